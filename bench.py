@@ -1,0 +1,226 @@
+"""Headline benchmark: Llama-3.3-70B (Q4_K, random-init) decode tok/s at batch 32
+and batch 1, plus p50 TTFT of a 2048-token prompt, on N B200s of one node.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...       (N > 1)
+
+N = 1: the whole model on one GPU.  N > 1: pipeline stages over NCCL p2p
+(``swarmllm_b200.parallel.pipeline``), weak scaling: 32 sequences per stage
+in flight (global batch 32*N), micro-batched so every stage is busy.
+
+`value` is device time: CUDA events around exactly K decode steps on the
+launching stream, bracketed by barrier + synchronize, max over ranks.
+`e2e` is the same metric through the public engine API (`LLMEngine.step` /
+`PipelineEngine.step`), whose timed region includes the H2D copy of each
+step's inputs from pinned memory and the D2H read of the sampled tokens.
+Workload: synthetic uniform-random token ids, random-init weights of the
+named architecture (no network for checkpoints).  The 40 GB of weights read
+per step are far larger than L2 (126 MB), so no L2 flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BASELINE_70B_TOKS = 4.1  # reference's published 70B decode tok/s (README.md:186, WAN, 3 computers)
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--model", default="llama-3.3-70b")
+    p.add_argument("--batch", type=int, default=32)
+    p.add_argument("--prompt", type=int, default=2048)
+    p.add_argument("--gen", type=int, default=512)
+    p.add_argument("--ttft-reps", type=int, default=3)
+    p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the headline)")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        mhz = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for i, n in enumerate(names):
+                if len(s) > 5 + i and s[5 + i].lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(self.samples)}
+
+
+def reference_arm(args):
+    print(json.dumps({"impl": "reference", "unavailable":
+                      "reference is a Rust/candle crate with no Python package; it cannot be "
+                      "pip-installed into baseline/_ref and no cargo/rustc toolchain or crates "
+                      "registry exists offline"}))
+
+
+def single_gpu(args):
+    import numpy as np
+    import torch
+
+    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from swarmllm_b200.models.config import preset
+
+    cfg = preset(args.model)
+    if args.layers:
+        cfg = cfg.scaled(n_layers=args.layers)
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    B, P, G = args.batch, args.prompt, args.gen
+    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=B, max_step_tokens=P,
+                        prefill_chunk=P, graph_sizes=(1, B))
+    t0 = time.time()
+    eng = LLMEngine.from_config(cfg, dev, ecfg, seed=1234)
+    t_init = time.time() - t0
+    rng = np.random.default_rng(0)
+    sp = SamplingParams(max_tokens=G, ignore_eos=True)
+
+    # ---- p50 TTFT: one 2048-token prompt alone, through the public API
+    ttfts = []
+    for r in range(args.ttft_reps + 1):
+        prompt = rng.integers(0, cfg.vocab, P).tolist()
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        rid = eng.add_request(prompt, SamplingParams(max_tokens=1, ignore_eos=True))
+        while True:
+            outs = eng.step()
+            if any(o[0] == rid for o in outs):
+                break
+        ttfts.append((time.perf_counter() - t) * 1e3)
+        eng.release(rid)
+    ttft_p50 = statistics.median(ttfts[1:])  # first run includes one-time setup
+
+    def decode_rate(batch: int, steps: int, warmup: int):
+        rids = [eng.add_request(rng.integers(0, cfg.vocab, P).tolist(), sp) for _ in range(batch)]
+        # run until every sequence is decoding
+        while eng.sched.num_waiting or any(len(eng.output(r)) == 0 for r in rids):
+            eng.step()
+        for _ in range(warmup):
+            eng.step()
+        runner = eng.runner
+        g, _, _ = runner.graphs[batch]
+        # device-timed: K graph replays of the decode step (inputs already resident)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])
+                          if os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0].isdigit() else 0) as cs:
+            a.record()
+            for _ in range(steps):
+                g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            dev_ms = a.elapsed_time(b)
+            # end to end through the public API (H2D inputs + D2H tokens every step)
+            torch.cuda.synchronize()
+            t = time.perf_counter()
+            for _ in range(steps):
+                eng.step()
+            e2e_s = time.perf_counter() - t
+        for r in rids:
+            eng.abort(r)
+            eng.release(r)
+        return dev_ms, e2e_s, cs.summary(), runner.h2d_bytes, runner.d2h_bytes
+
+    ms32, e2e32, clocks, h2d, d2h = decode_rate(B, args.steps, args.warmup)
+    ms1, e2e1, _, _, _ = decode_rate(1, args.steps, args.warmup)
+    value = B * args.steps / (ms32 / 1e3)
+    launches = kernel_launches_per_step(eng.model) * args.steps
+    line = {
+        "metric": f"decode tok/s at batch {B} (aggregate), Llama-3.3-70B Q4_K",
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms32 / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": round(value / BASELINE_70B_TOKS, 2), "dtype": "fp16 activations, fp32 accumulate, Q4_K weights",
+        "data": "synthetic uniform-random token ids; random-init Q4_K weights (llama-3.3-70b architecture)",
+        "config": {"model": cfg.name, "layers": cfg.n_layers, "global_batch": B, "seq_len": P,
+                   "gen_len": G, "parallelism": "single GPU", "kv": "paged fp16, 16-token pages",
+                   "l2": "no flush: 40 GB of weights streamed per step >> 126 MB L2"},
+        "decode_tok_s_batch1": round(args.steps / (ms1 / 1e3), 2),
+        "ms_per_step_batch1": round(ms1 / args.steps, 4),
+        "ttft_p50_ms": round(ttft_p50, 2), "ttft_prompt_tokens": P,
+        "e2e": {"value": round(B * args.steps / e2e32, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "batch1_value": round(args.steps / e2e1, 2)},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "init_s": round(t_init, 1),
+    }
+    if args.layers:
+        line["invalid"] = "layer count overridden (debug)"
+    print(json.dumps(line), flush=True)
+
+
+def kernel_launches_per_step(model) -> int:
+    """Our kernels per decode forward: embed + rmsnorm, per layer 4 GEMMs +
+    4 epilogues + attention split + combine, then head GEMM + logits copy +
+    row gather + argmax."""
+    n = 2 + 10 * len(model.layers)
+    if model.last:
+        n += 3  # head GEMM, logits epilogue, argmax (the row gather is a torch op)
+    return n
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        return single_gpu(args)
+    from swarmllm_b200.parallel.bench_pp import pipeline_bench
+    return pipeline_bench(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,235 @@
+// PyTorch bindings for the sm_100a kernels (module swarmllm_b200._C).
+// Every op launches on torch's current CUDA stream, so they can be captured in
+// CUDA graphs.  Shapes and dtypes are checked here; the kernels trust them.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "kernels.h"
+#include "gemm_out.cuh"
+
+namespace py = pybind11;
+using at::Tensor;
+using OptT = std::optional<Tensor>;
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+#define CHECK_DT(x, dt) TORCH_CHECK((x).scalar_type() == (dt), #x " has wrong dtype")
+
+static cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+template <typename T>
+static T* ptr_or_null(const OptT& t) {
+  return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+// A GEMM result: the fp32 workspace plus how to read it (see gemm_out.cuh).
+struct GemmResult {
+  swarm::GemmOut g{};
+  Tensor ws;  // keeps the buffer alive
+};
+
+static int num_sms_of(const Tensor& t) {
+  static int cached[64] = {0};
+  int dev = t.get_device();
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    cudaDeviceProp p;
+    cudaGetDeviceProperties(&p, dev);
+    cached[dev] = p.multiProcessorCount;
+  }
+  return cached[dev];
+}
+
+// ---------------------------------------------------------------- elementwise
+void embed_gather(Tensor table, int64_t type, int64_t hidden, Tensor ids, Tensor out) {
+  CHECK_CUDA(table); CHECK_CUDA(ids); CHECK_CUDA(out);
+  CHECK_DT(ids, at::kInt); CHECK_DT(out, at::kFloat);
+  const at::cuda::CUDAGuard guard(out.device());
+  launch_embed_gather(table.data_ptr(), (int)type, (int)hidden, ids.data_ptr<int32_t>(),
+                      (int)ids.numel(), out.data_ptr<float>(), cur_stream());
+}
+
+void rmsnorm(Tensor x, Tensor w, Tensor out, double eps) {
+  CHECK_CUDA(x); CHECK_DT(x, at::kFloat); CHECK_DT(w, at::kFloat); CHECK_DT(out, at::kHalf);
+  CHECK_CONTIG(x); CHECK_CONTIG(out);
+  const at::cuda::CUDAGuard guard(x.device());
+  const int dim = (int)x.size(-1);
+  launch_rmsnorm(x.data_ptr<float>(), w.data_ptr<float>(),
+                 reinterpret_cast<__half*>(out.data_ptr()), (int)(x.numel() / dim), dim,
+                 (float)eps, cur_stream());
+}
+
+void epi_residual_rmsnorm(const GemmResult& g, Tensor residual, OptT bias, Tensor w, OptT out,
+                          double eps) {
+  CHECK_DT(residual, at::kFloat);
+  TORCH_CHECK(residual.size(-1) == g.g.rows, "residual width != GEMM rows");
+  const at::cuda::CUDAGuard guard(residual.device());
+  launch_epi_residual_rmsnorm(g.g, residual.data_ptr<float>(), ptr_or_null<float>(bias),
+                              w.data_ptr<float>(), ptr_or_null<__half>(out), (float)eps,
+                              out.has_value() ? (int)out->stride(0) : 0, cur_stream());
+}
+
+void epi_rope_kv(const GemmResult& g, OptT bias, Tensor positions, OptT slots, Tensor inv_freq,
+                 int64_t n_q, int64_t n_kv, int64_t head_dim, int64_t rope_dim, bool neox,
+                 double attn_factor, Tensor q_out, OptT k_cache, OptT v_cache, int64_t page_size,
+                 OptT q_norm_w, OptT k_norm_w, double norm_eps) {
+  CHECK_DT(positions, at::kInt); CHECK_DT(q_out, at::kHalf); CHECK_DT(inv_freq, at::kFloat);
+  TORCH_CHECK(g.g.rows == (n_q + 2 * n_kv) * head_dim, "QKV rows mismatch");
+  const at::cuda::CUDAGuard guard(q_out.device());
+  launch_epi_rope_kv(g.g, ptr_or_null<float>(bias), positions.data_ptr<int32_t>(),
+                     ptr_or_null<int32_t>(slots), inv_freq.data_ptr<float>(), (int)n_q, (int)n_kv,
+                     (int)head_dim, (int)rope_dim, neox ? 1 : 0, (float)attn_factor,
+                     reinterpret_cast<__half*>(q_out.data_ptr()), ptr_or_null<__half>(k_cache),
+                     ptr_or_null<__half>(v_cache), (int)page_size, ptr_or_null<float>(q_norm_w),
+                     ptr_or_null<float>(k_norm_w), (float)norm_eps, cur_stream());
+}
+
+void epi_swiglu(const GemmResult& g, OptT bias, int64_t F, int64_t kind, bool interleaved,
+                double alpha, double limit, Tensor out) {
+  CHECK_DT(out, at::kHalf);
+  TORCH_CHECK(g.g.rows == 2 * F, "gate_up rows must be 2F");
+  const at::cuda::CUDAGuard guard(out.device());
+  launch_epi_swiglu(g.g, ptr_or_null<float>(bias), (int)F, (int)kind, interleaved ? 1 : 0,
+                    (float)alpha, (float)limit, reinterpret_cast<__half*>(out.data_ptr()),
+                    cur_stream());
+}
+
+void epi_copy(const GemmResult& g, OptT bias, Tensor out) {
+  CHECK_DT(out, at::kFloat);
+  const at::cuda::CUDAGuard guard(out.device());
+  launch_epi_copy(g.g, ptr_or_null<float>(bias), out.data_ptr<float>(), (int)out.stride(0),
+                  cur_stream());
+}
+
+// ---------------------------------------------------------------- GEMMs
+GemmResult qmatmul_simt(Tensor w, int64_t type, int64_t rows, int64_t K, Tensor x, Tensor out) {
+  CHECK_CUDA(w); CHECK_CUDA(x); CHECK_DT(x, at::kHalf); CHECK_DT(out, at::kFloat);
+  TORCH_CHECK(x.size(-1) == K && x.stride(-1) == 1, "x must be [T, K] with unit inner stride");
+  TORCH_CHECK(out.size(-1) == rows && out.is_contiguous(), "out must be [T, rows] contiguous");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int T = (int)x.size(0);
+  int rc = launch_qmatmul_simt(w.data_ptr(), (int)type, (int)rows, (int)K,
+                               reinterpret_cast<const __half*>(x.data_ptr()), (int)x.stride(0), T,
+                               out.data_ptr<float>(), (int)rows, cur_stream());
+  TORCH_CHECK(rc == 0, "qmatmul_simt: unsupported type ", type);
+  GemmResult r;
+  r.g.ws = out.data_ptr<float>();
+  r.g.rows = (int)rows;
+  r.g.T = T;
+  r.g.mode = 0;
+  r.ws = out;
+  return r;
+}
+
+py::tuple q4k_tc_plan_py(int64_t rows, int64_t K, int64_t T, int64_t num_sms) {
+  int N, ntt, kb, upc, ctas;
+  long total;
+  size_t need;
+  q4k_tc_plan((int)rows, (int)K, (int)T, (int)num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need);
+  return py::make_tuple(N, ntt, kb, total, upc, ctas, need);
+}
+
+GemmResult qgemm_q4k_tc(Tensor w_packed, int64_t rows, int64_t K, Tensor x, Tensor ws,
+                        Tensor status, int64_t num_sms) {
+  CHECK_CUDA(w_packed); CHECK_CUDA(x); CHECK_DT(x, at::kHalf); CHECK_DT(ws, at::kFloat);
+  CHECK_DT(status, at::kInt);
+  TORCH_CHECK(x.size(-1) == K && x.stride(-1) == 1, "x must be [T, K] with unit inner stride");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int T = (int)x.size(0);
+  if (num_sms <= 0) num_sms = num_sms_of(x);
+  GemmResult r;
+  int rc = launch_qgemm_q4k_tc(w_packed.data_ptr(), (int)rows, (int)K,
+                               reinterpret_cast<const __half*>(x.data_ptr()), (int)x.stride(0), T,
+                               ws.data_ptr<float>(), (size_t)ws.numel(), (int)num_sms,
+                               status.data_ptr<int>(), &r.g, cur_stream());
+  TORCH_CHECK(rc == 0, "qgemm_q4k_tc launch failed: rc=", rc);
+  r.ws = ws;
+  return r;
+}
+
+void q4k_repack(Tensor src, int64_t rows, int64_t K, Tensor dst) {
+  CHECK_CUDA(src); CHECK_CUDA(dst);
+  TORCH_CHECK(K % 256 == 0, "K must be a multiple of 256");
+  const int64_t rows_pad = (rows + 127) / 128 * 128;
+  TORCH_CHECK(dst.numel() * dst.element_size() >= rows_pad * (K / 256) * 144, "dst too small");
+  const at::cuda::CUDAGuard guard(dst.device());
+  TORCH_CHECK(launch_q4k_repack(src.data_ptr(), (int)rows, (int)K, dst.data_ptr(), cur_stream()) == 0,
+              "repack launch failed");
+}
+
+// ---------------------------------------------------------------- attention
+void decode_attn(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor seq_lens,
+                 OptT tree_mask, OptT tree_start, OptT sinks, int64_t window, double scale,
+                 double softcap, int64_t keys_per_split, Tensor part_o, Tensor part_ml,
+                 Tensor out) {
+  CHECK_DT(q, at::kHalf); CHECK_DT(k_cache, at::kHalf); CHECK_DT(v_cache, at::kHalf);
+  CHECK_DT(block_table, at::kInt); CHECK_DT(seq_lens, at::kInt); CHECK_DT(out, at::kHalf);
+  CHECK_CONTIG(q); CHECK_CONTIG(out); CHECK_CONTIG(block_table);
+  const at::cuda::CUDAGuard guard(q.device());
+  const int T = (int)q.size(0), n_q = (int)q.size(1), d = (int)q.size(2);
+  const int n_kv = (int)k_cache.size(1), page = (int)k_cache.size(2);
+  const int n_splits = (int)part_ml.size(2);
+  TORCH_CHECK(part_o.size(2) == n_splits && part_o.size(3) == d, "part_o shape");
+  int rc = launch_decode_attn_simt(
+      reinterpret_cast<const __half*>(q.data_ptr()),
+      reinterpret_cast<const __half*>(k_cache.data_ptr()),
+      reinterpret_cast<const __half*>(v_cache.data_ptr()), block_table.data_ptr<int32_t>(),
+      (int)block_table.stride(0), seq_lens.data_ptr<int32_t>(),
+      ptr_or_null<uint64_t>(tree_mask), ptr_or_null<int32_t>(tree_start), ptr_or_null<float>(sinks),
+      T, n_q, n_kv, d, page, (int)window, (float)scale, (float)softcap, (int)keys_per_split,
+      n_splits, part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+      reinterpret_cast<__half*>(out.data_ptr()), cur_stream());
+  TORCH_CHECK(rc == 0, "decode_attn: unsupported head_dim/group size");
+}
+
+// ---------------------------------------------------------------- sampling
+void argmax(Tensor logits, Tensor out, OptT out_val) {
+  CHECK_DT(logits, at::kFloat); CHECK_DT(out, at::kInt);
+  const at::cuda::CUDAGuard guard(logits.device());
+  launch_argmax(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1),
+                (int)logits.stride(0), out.data_ptr<int32_t>(), ptr_or_null<float>(out_val),
+                cur_stream());
+}
+
+void sample(Tensor logits, Tensor temperature, OptT top_k, OptT top_p, OptT seeds, OptT positions,
+            Tensor out) {
+  CHECK_DT(logits, at::kFloat); CHECK_DT(out, at::kInt); CHECK_DT(temperature, at::kFloat);
+  const at::cuda::CUDAGuard guard(logits.device());
+  launch_sample(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1),
+                (int)logits.stride(0), temperature.data_ptr<float>(), ptr_or_null<int32_t>(top_k),
+                ptr_or_null<float>(top_p), ptr_or_null<uint64_t>(seeds),
+                ptr_or_null<int32_t>(positions), out.data_ptr<int32_t>(), cur_stream());
+}
+
+void philox_uniform(int64_t seed, Tensor positions, int64_t V, Tensor out) {
+  const at::cuda::CUDAGuard guard(out.device());
+  launch_philox_uniform((uint64_t)seed, positions.data_ptr<int32_t>(), (int)positions.numel(),
+                        (int)V, out.data_ptr<float>(), cur_stream());
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "swarmllm_b200 sm_100a kernels";
+  py::class_<GemmResult>(m, "GemmResult")
+      .def_property_readonly("rows", [](const GemmResult& r) { return r.g.rows; })
+      .def_property_readonly("T", [](const GemmResult& r) { return r.g.T; })
+      .def_property_readonly("mode", [](const GemmResult& r) { return r.g.mode; })
+      .def_property_readonly("tok_tile", [](const GemmResult& r) { return r.g.tok_tile; })
+      .def_property_readonly("upc", [](const GemmResult& r) { return r.g.upc; })
+      .def_property_readonly("ksb", [](const GemmResult& r) { return r.g.ksb; })
+      .def_readonly("ws", &GemmResult::ws);
+  m.def("embed_gather", &embed_gather);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("epi_residual_rmsnorm", &epi_residual_rmsnorm);
+  m.def("epi_rope_kv", &epi_rope_kv);
+  m.def("epi_swiglu", &epi_swiglu);
+  m.def("epi_copy", &epi_copy);
+  m.def("qmatmul_simt", &qmatmul_simt);
+  m.def("q4k_tc_plan", &q4k_tc_plan_py);
+  m.def("qgemm_q4k_tc", &qgemm_q4k_tc);
+  m.def("q4k_repack", &q4k_repack);
+  m.def("decode_attn", &decode_attn);
+  m.def("argmax", &argmax);
+  m.def("sample", &sample);
+  m.def("philox_uniform", &philox_uniform);
+}

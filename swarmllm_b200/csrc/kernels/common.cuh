@@ -1,0 +1,82 @@
+// Shared device helpers for the sm_100a kernels of swarmllm_b200.
+//
+// Every kernel in this directory is plain CUDA C++ with no torch headers; the
+// launchers take raw device pointers plus a cudaStream_t and are bound to
+// PyTorch in csrc/bindings/torch_ops.cpp.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#define SW_DEVICE __device__ __forceinline__
+#define SW_HOST_DEVICE __host__ __device__ __forceinline__
+
+namespace swarm {
+
+constexpr int kWarp = 32;
+
+SW_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+SW_DEVICE float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum; `smem` must hold >= 32 floats.  All threads get the result.
+SW_DEVICE float block_sum(float v, float* smem) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) smem[wid] = v;
+  __syncthreads();
+  float r = (threadIdx.x < nw) ? smem[threadIdx.x] : 0.f;
+  if (wid == 0) {
+    r = warp_sum(r);
+    if (lane == 0) smem[0] = r;
+  }
+  __syncthreads();
+  return smem[0];
+}
+
+SW_DEVICE float block_max(float v, float* smem) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nw = (blockDim.x + 31) >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) smem[wid] = v;
+  __syncthreads();
+  float r = (threadIdx.x < nw) ? smem[threadIdx.x] : -INFINITY;
+  if (wid == 0) {
+    r = warp_max(r);
+    if (lane == 0) smem[0] = r;
+  }
+  __syncthreads();
+  return smem[0];
+}
+
+SW_DEVICE float to_f(float x) { return x; }
+SW_DEVICE float to_f(__half x) { return __half2float(x); }
+SW_DEVICE float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T> SW_DEVICE T from_f(float x);
+template <> SW_DEVICE float from_f<float>(float x) { return x; }
+template <> SW_DEVICE __half from_f<__half>(float x) { return __float2half_rn(x); }
+template <> SW_DEVICE __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// Half stored as raw uint16 bits (GGUF block scales).
+SW_DEVICE float half_bits_to_f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+SW_DEVICE float silu(float x) { return x / (1.f + __expf(-x)); }
+
+}  // namespace swarm
+
+// Host-side launch check: records the last launch error without syncing.
+#define SW_LAUNCH_CHECK() do { (void)cudaPeekAtLastError(); } while (0)

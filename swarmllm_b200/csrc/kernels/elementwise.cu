@@ -1,0 +1,265 @@
+// Embedding gather, RMSNorm and the GEMM epilogues that fuse the small ops of
+// a decoder layer into the kernel that reads the GEMM result:
+//
+//   embed_gather          token ids -> fp32 residual rows (any GGML table type)
+//   rmsnorm               fp32 residual -> bf16 normed (GEMM input)
+//   epi_residual_rmsnorm  residual += GEMM out; normed = RMSNorm(residual) * w
+//                         (replaces the reference's add_rmsnorm_f32,
+//                          kernels/fused_decode.cu:119, plus the o/down-proj add)
+//   epi_rope_kv           q,k,v from the QKV GEMM: bias, RoPE (GGML "norm"
+//                         interleaved pairs or NEOX halves, partial rotary), q ->
+//                         bf16, k,v -> fp16 paged cache pages
+//                         (replaces heads_first_f32 + rope_partial_f32 +
+//                          kv_write_f16: kernels/fused_decode.cu:185,240,
+//                          kernels/kv_append.cu:33)
+//   epi_swiglu            silu(gate) * up, or gpt-oss clamped SwiGLU
+//                         (kernels/fused_decode.cu:47,68)
+//   epi_copy              GEMM out -> dense fp32 (logits)
+#include "kernels.h"
+#include "gemm_out.cuh"
+#include "quant_blocks.cuh"
+
+namespace swarm {
+
+__global__ void embed_gather_kernel(const uint8_t* __restrict__ table, int type, int hidden,
+                                    const int32_t* __restrict__ ids, float* __restrict__ out) {
+  const int t = blockIdx.x;
+  const int id = ids[t];
+  const int bv = ggml_block_values(type), bb = ggml_block_bytes(type);
+  const size_t row_bytes = (size_t)(hidden / bv) * bb;
+  const uint8_t* row = table + (size_t)id * row_bytes;
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const int blk = i / bv;
+    out[(size_t)t * hidden + i] = dequant_one(type, row + (size_t)blk * bb, i - blk * bv);
+  }
+}
+
+template <int kThreads>
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                               __half* __restrict__ out, int dim, float eps) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const float* xr = x + (size_t)t * dim;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += kThreads) ss += xr[i] * xr[i];
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / dim + eps);
+  for (int i = threadIdx.x; i < dim; i += kThreads)
+    out[(size_t)t * dim + i] = __float2half_rn(xr[i] * inv * w[i]);
+}
+
+// One CTA per token.  The residual row is staged in shared memory so the
+// GEMM partials are read exactly once.
+template <int kThreads>
+__global__ void epi_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ residual,
+                                            const float* __restrict__ bias,
+                                            const float* __restrict__ w,
+                                            __half* __restrict__ out, float eps,
+                                            int out_stride) {
+  extern __shared__ float row[];
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const int dim = g.rows;
+  float* rr = residual + (size_t)t * dim;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += kThreads) {
+    float v = rr[i] + g.get(t, i) + (bias ? bias[i] : 0.f);
+    rr[i] = v;
+    row[i] = v;
+    ss += v * v;
+  }
+  if (out == nullptr) return;
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / dim + eps);
+  for (int i = threadIdx.x; i < dim; i += kThreads)
+    out[(size_t)t * out_stride + i] = __float2half_rn(row[i] * inv * w[i]);
+}
+
+// One CTA per token; threads walk (head, pair).  Layout of the QKV GEMM rows:
+// [q heads][k heads][v heads], each head_dim wide.
+// Cache layout: [pages][n_kv][page_size][head_dim] fp16.
+__global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
+                                   const int32_t* __restrict__ positions,
+                                   const int32_t* __restrict__ slots,
+                                   const float* __restrict__ inv_freq, int n_q, int n_kv,
+                                   int head_dim, int rope_dim, int neox, float attn_factor,
+                                   __half* __restrict__ q_out, __half* __restrict__ k_cache,
+                                   __half* __restrict__ v_cache, int page_size,
+                                   const float* __restrict__ q_norm_w,
+                                   const float* __restrict__ k_norm_w, float norm_eps) {
+  extern __shared__ float sh[];  // (n_q + n_kv) * head_dim floats
+  const int t = blockIdx.x;
+  const int pos = positions[t];
+  const int slot = slots ? slots[t] : -1;
+  const int qk_rows = (n_q + n_kv) * head_dim;
+  const int total = (n_q + 2 * n_kv) * head_dim;
+  // Stage q and k (pre-RoPE) in shared memory; write v straight to the cache.
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    float v = g.get(t, i) + (bias ? bias[i] : 0.f);
+    if (i < qk_rows) {
+      sh[i] = v;
+    } else if (slot >= 0) {
+      const int j = i - qk_rows, h = j / head_dim, d = j - h * head_dim;
+      const int page = slot / page_size, off = slot - page * page_size;
+      v_cache[(((size_t)page * n_kv + h) * page_size + off) * head_dim + d] = __float2half_rn(v);
+    }
+  }
+  __syncthreads();
+  // Optional per-head RMSNorm of q and k (Qwen3-style qk-norm); one warp per head.
+  if (q_norm_w != nullptr) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int h = warp; h < n_q + n_kv; h += nw) {
+      float* x = sh + h * head_dim;
+      float s = 0.f;
+      for (int d = lane; d < head_dim; d += 32) s += x[d] * x[d];
+      s = warp_sum(s);
+      const float inv = rsqrtf(s / head_dim + norm_eps);
+      const float* wn = (h < n_q) ? q_norm_w : k_norm_w;
+      for (int d = lane; d < head_dim; d += 32) x[d] = x[d] * inv * wn[d];
+    }
+    __syncthreads();
+  }
+  const int half = rope_dim / 2;
+  // Rotate pairs; unrotated tail dims are copied.
+  for (int i = threadIdx.x; i < (n_q + n_kv) * head_dim; i += blockDim.x) {
+    const int h = i / head_dim, d = i - h * head_dim;
+    const float* x = sh + h * head_dim;
+    float y;
+    if (d < rope_dim) {
+      int fi, partner;
+      bool first;
+      if (neox) {
+        fi = (d < half) ? d : d - half;
+        first = d < half;
+        partner = first ? d + half : d - half;
+      } else {
+        fi = d >> 1;
+        first = (d & 1) == 0;
+        partner = first ? d + 1 : d - 1;
+      }
+      float s, c;
+      sincosf((float)pos * inv_freq[fi], &s, &c);
+      c *= attn_factor;
+      s *= attn_factor;
+      y = first ? (x[d] * c - x[partner] * s) : (x[partner] * s + x[d] * c);
+    } else {
+      y = x[d];
+    }
+    if (h < n_q) {
+      q_out[((size_t)t * n_q + h) * head_dim + d] = __float2half_rn(y);
+    } else if (slot >= 0) {
+      const int hk = h - n_q;
+      const int page = slot / page_size, off = slot - page * page_size;
+      k_cache[(((size_t)page * n_kv + hk) * page_size + off) * head_dim + d] = __float2half_rn(y);
+    }
+  }
+}
+
+// rows [0, F) are gate, [F, 2F) are up (or interleaved for gpt-oss: even=gate,
+// odd=up when `interleaved`).  kind 0: silu(g)*u.  kind 1: gpt-oss clamped
+// SwiGLU x=min(g,limit), u=clamp(u,-limit,limit), x*sigmoid(alpha*x)*(u+1).
+__global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int F, int kind,
+                                  int interleaved, float alpha, float limit,
+                                  __half* __restrict__ out) {
+  const int t = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < F; i += gridDim.x * blockDim.x) {
+    const int rg = interleaved ? 2 * i : i;
+    const int ru = interleaved ? 2 * i + 1 : F + i;
+    float gv = g.get(t, rg) + (bias ? bias[rg] : 0.f);
+    float uv = g.get(t, ru) + (bias ? bias[ru] : 0.f);
+    float y;
+    if (kind == 0) {
+      y = silu(gv) * uv;
+    } else {
+      gv = fminf(gv, limit);
+      uv = fminf(fmaxf(uv, -limit), limit);
+      y = gv / (1.f + __expf(-alpha * gv)) * (uv + 1.f);
+    }
+    out[(size_t)t * F + i] = __float2half_rn(y);
+  }
+}
+
+__global__ void epi_copy_kernel(GemmOut g, const float* __restrict__ bias, float* __restrict__ out,
+                                int out_stride) {
+  const int t = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < g.rows; i += gridDim.x * blockDim.x)
+    out[(size_t)t * out_stride + i] = g.get(t, i) + (bias ? bias[i] : 0.f);
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y,
+                                   size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    y[i] = __float2half_rn(x[i]);
+}
+
+}  // namespace swarm
+
+using namespace swarm;
+
+void launch_embed_gather(const void* table, int type, int hidden, const int32_t* ids, int n,
+                         float* out, cudaStream_t s) {
+  if (n <= 0) return;
+  embed_gather_kernel<<<n, 256, 0, s>>>((const uint8_t*)table, type, hidden, ids, out);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_rmsnorm(const float* x, const float* w, __half* out, int rows, int dim,
+                    float eps, cudaStream_t s) {
+  if (rows <= 0) return;
+  rmsnorm_kernel<512><<<rows, 512, 0, s>>>(x, w, out, dim, eps);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_epi_residual_rmsnorm(const GemmOut& g, float* residual, const float* bias,
+                                 const float* w, __half* out, float eps, int out_stride,
+                                 cudaStream_t s) {
+  if (g.T <= 0) return;
+  size_t sm = (size_t)g.rows * sizeof(float);
+  if (sm > 48 * 1024)
+    cudaFuncSetAttribute(epi_residual_rmsnorm_kernel<512>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  epi_residual_rmsnorm_kernel<512><<<g.T, 512, sm, s>>>(g, residual, bias, w, out, eps,
+                                                        out_stride ? out_stride : g.rows);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_epi_rope_kv(const GemmOut& g, const float* bias, const int32_t* positions,
+                        const int32_t* slots, const float* inv_freq, int n_q, int n_kv,
+                        int head_dim, int rope_dim, int neox, float attn_factor,
+                        __half* q_out, __half* k_cache, __half* v_cache, int page_size,
+                        const float* q_norm_w, const float* k_norm_w, float norm_eps,
+                        cudaStream_t s) {
+  if (g.T <= 0) return;
+  size_t sm = (size_t)(n_q + n_kv) * head_dim * sizeof(float);
+  if (sm > 48 * 1024)
+    cudaFuncSetAttribute(epi_rope_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sm);
+  epi_rope_kv_kernel<<<g.T, 256, sm, s>>>(g, bias, positions, slots, inv_freq, n_q, n_kv,
+                                          head_dim, rope_dim, neox, attn_factor, q_out, k_cache,
+                                          v_cache, page_size, q_norm_w, k_norm_w, norm_eps);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_epi_swiglu(const GemmOut& g, const float* bias, int F, int kind, int interleaved,
+                       float alpha, float limit, __half* out, cudaStream_t s) {
+  if (g.T <= 0) return;
+  dim3 grid((F + 255) / 256 < 64 ? (F + 255) / 256 : 64, g.T);
+  epi_swiglu_kernel<<<grid, 256, 0, s>>>(g, bias, F, kind, interleaved, alpha, limit, out);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_epi_copy(const GemmOut& g, const float* bias, float* out, int out_stride,
+                     cudaStream_t s) {
+  if (g.T <= 0) return;
+  dim3 grid((g.rows + 255) / 256 < 256 ? (g.rows + 255) / 256 : 256, g.T);
+  epi_copy_kernel<<<grid, 256, 0, s>>>(g, bias, out, out_stride ? out_stride : g.rows);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s) {
+  if (n == 0) return;
+  int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+  f32_to_f16_kernel<<<blocks, 256, 0, s>>>(x, y, n);
+  SW_LAUNCH_CHECK();
+}

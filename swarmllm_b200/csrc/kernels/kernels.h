@@ -1,0 +1,64 @@
+// Host-side launchers of the sm_100a kernels.  Plain pointers + stream; no
+// torch types, so the kernels build without torch headers and the same entry
+// points can be called from C/C++ hosts.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace swarm {
+struct GemmOut;
+}
+
+// ---- elementwise / epilogues (elementwise.cu) ------------------------------
+void launch_embed_gather(const void* table, int type, int hidden, const int32_t* ids, int n,
+                         float* out, cudaStream_t s);
+void launch_rmsnorm(const float* x, const float* w, __half* out, int rows, int dim, float eps,
+                    cudaStream_t s);
+void launch_epi_residual_rmsnorm(const swarm::GemmOut& g, float* residual, const float* bias,
+                                 const float* w, __half* out, float eps, int out_stride,
+                                 cudaStream_t s);
+void launch_epi_rope_kv(const swarm::GemmOut& g, const float* bias, const int32_t* positions,
+                        const int32_t* slots, const float* inv_freq, int n_q, int n_kv,
+                        int head_dim, int rope_dim, int neox, float attn_factor, __half* q_out,
+                        __half* k_cache, __half* v_cache, int page_size, const float* q_norm_w,
+                        const float* k_norm_w, float norm_eps, cudaStream_t s);
+void launch_epi_swiglu(const swarm::GemmOut& g, const float* bias, int F, int kind,
+                       int interleaved, float alpha, float limit, __half* out, cudaStream_t s);
+void launch_epi_copy(const swarm::GemmOut& g, const float* bias, float* out, int out_stride,
+                     cudaStream_t s);
+void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
+
+// ---- quantized GEMM ---------------------------------------------------------
+int launch_qmatmul_simt(const void* w, int type, int rows, int K, const __half* x, int x_stride,
+                        int T, float* out, int out_stride, cudaStream_t s);
+int q4k_tc_tok_tile(int T);
+void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* ksb,
+                 long* total_units, int* upc, int* n_ctas, size_t* ws_floats);
+int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, int x_stride,
+                        int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
+                        swarm::GemmOut* out, cudaStream_t s);
+int launch_q4k_repack(const void* src, int rows, int K, void* dst, cudaStream_t s);
+int make_tmap_2d_16bit(CUtensorMap* map, const void* base, int rows, int cols, int row_stride,
+                       int box_rows, int box_cols, int swizzle_bytes);
+
+// ---- attention --------------------------------------------------------------
+int launch_decode_attn_simt(const __half* q, const __half* k_cache, const __half* v_cache,
+                            const int32_t* block_table, int bt_stride, const int32_t* seq_lens,
+                            const uint64_t* tree_mask, const int32_t* tree_start,
+                            const float* sinks, int T, int n_q, int n_kv, int head_dim,
+                            int page_size, int window, float scale, float softcap,
+                            int keys_per_split, int n_splits, float* part_o, float* part_ml,
+                            __half* out, cudaStream_t s);
+
+// ---- sampling -----------------------------------------------------------------
+void launch_argmax(const float* logits, int rows, int V, int stride, int32_t* out, float* out_val,
+                   cudaStream_t s);
+void launch_sample(const float* logits, int rows, int V, int stride, const float* temperature,
+                   const int32_t* top_k, const float* top_p, const uint64_t* seeds,
+                   const int32_t* positions, int32_t* out, cudaStream_t s);
+void launch_philox_uniform(uint64_t seed, const int32_t* positions, int n_pos, int V, float* out,
+                           cudaStream_t s);

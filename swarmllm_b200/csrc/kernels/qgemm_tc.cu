@@ -1,0 +1,475 @@
+// Q4_K x fp16 GEMM on the 5th-generation tensor cores (tcgen05 / TMEM / TMA).
+//
+//   out[t][r] = sum_k W[r][k] * X[t][k],   W: Q4_K (repacked), X: fp16 [T, K]
+//
+// One kernel serves decode (T = 1..256 tokens, weight-streaming, bound by HBM)
+// and prefill (T up to thousands, tensor-bound).  It replaces the reference's
+// three quantized paths (candle mmvq dp4a for <= 8 rows, llama.cpp MMQ
+// mma.sync int8, and dequantize-to-f16 + cuBLAS for >= 64 rows:
+// vendor/candle/candle-core/src/quantized/cuda.rs:291,519,1005).
+//
+// Design (swap-AB weight streaming):
+//  * The MMA's M dimension is 128 weight rows; N is the token tile (16..256).
+//  * Weights are repacked once at load time (launch_q4k_repack) into
+//    [row_tile][superblock][128 rows][144 B]: 128 B of 4-bit codes whose
+//    nibbles are ordered so that one LOP3 yields two consecutive K values as
+//    an fp16 pair (1024 + q) -- then an exact subtract and one HFMA2 apply the
+//    6-bit sub-block scale and min -- followed by the 16 B (d, dmin, scales).
+//    A 128-row x 256-K chunk is one contiguous 18 KB bulk copy.
+//  * Dequantizer warps (one thread per weight row) write the fp16 weights
+//    straight into TMEM and the MMA reads its A operand from TMEM
+//    (tcgen05.mma ... [a_tmem]); shared memory only carries the raw 4.5-bit
+//    codes and the activations, so it is not the bottleneck at decode.
+//  * Activations arrive by TMA (128 B swizzle, K-major canonical layout); the
+//    fp32 accumulator lives in TMEM columns [0, N).
+//  * Persistent, stream-K balanced: the (row_tile, token_tile, superblock)
+//    units are split evenly over the CTAs; each CTA writes one fp32 partial
+//    per tile it touched into workspace slot (tile + cta); epilogue kernels
+//    sum the slots while reading (gemm_out.cuh).
+//
+// Warp roles: warp 0 = bulk/TMA producer, warp 1 = TMEM owner + MMA issuer,
+// warps 2.. = 2 dequantizer warpgroups (alternate units), which also drain
+// the accumulator for the segments they finish.
+#include "kernels.h"
+#include "gemm_out.cuh"
+#include "tc_utils.cuh"
+
+namespace swarm {
+using namespace tc;
+
+constexpr int kQ4kRowBytes = 144;
+constexpr int kWStageBytes = 128 * kQ4kRowBytes;  // 18432
+constexpr int kTmemCols = 512;
+constexpr int kAColBase = 256;
+constexpr int kAStages = 4;  // 64 TMEM columns each = 128 K fp16 values
+constexpr int kDqWG = 2;     // dequantizer warpgroups
+constexpr int kGemmThreads = 64 + 128 * kDqWG;
+
+template <int N>
+struct QCfg {
+  static constexpr int X_HALF_BYTES = N * 256;
+  static constexpr int X_ST = N <= 64 ? 8 : (N <= 128 ? 4 : 2);
+  static constexpr int W_ST = 4;
+  static constexpr int X_BYTES = X_ST * X_HALF_BYTES;
+  static constexpr int W_BYTES = W_ST * kWStageBytes;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM = 1024 + X_BYTES + W_BYTES + BAR_BYTES;
+};
+
+struct QGemmArgs {
+  const uint8_t* w;
+  int rows, K, T;
+  int n_tok_tiles, ksb;
+  long total_units;
+  int upc;
+  float* ws;
+  int* status;
+};
+
+SW_DEVICE __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+SW_DEVICE uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// 8 permuted nibbles -> 4 fp16 pairs (K order), scale s, min mb.
+SW_DEVICE void dq_word(uint32_t x, __half2 S, __half2 S16, __half2 MB, uint32_t* out) {
+  const uint32_t MAGIC = 0x64006400u;
+  const __half2 K1024 = u32_as_h2(0x64006400u);
+  const uint32_t hi = x >> 8;
+  __half2 c0 = __hsub2(u32_as_h2((x & 0x000F000Fu) | MAGIC), K1024);
+  __half2 c1 = __hsub2(u32_as_h2((x & 0x00F000F0u) | MAGIC), K1024);
+  __half2 c2 = __hsub2(u32_as_h2((hi & 0x000F000Fu) | MAGIC), K1024);
+  __half2 c3 = __hsub2(u32_as_h2((hi & 0x00F000F0u) | MAGIC), K1024);
+  out[0] = h2_as_u32(__hfma2(c0, S, MB));
+  out[1] = h2_as_u32(__hfma2(c1, S16, MB));
+  out[2] = h2_as_u32(__hfma2(c2, S, MB));
+  out[3] = h2_as_u32(__hfma2(c3, S16, MB));
+}
+
+// (d*sc_j, dmin*m_j) for the 8 sub-blocks from the 16-byte header
+// {f16 d, f16 dmin, u8 scales[12]}; constant byte indices keep it in registers.
+SW_DEVICE void q4k_decode_scales(const uint4& hdr, float* s, float* mb) {
+  const float d = half_bits_to_f((uint16_t)(hdr.x & 0xFFFF));
+  const float dmin = half_bits_to_f((uint16_t)(hdr.x >> 16));
+  const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;
+#define SB(i) ((int)((((i) < 4 ? w0 : ((i) < 8 ? w1 : w2)) >> (8 * ((i) & 3))) & 0xFF))
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    int sc, m;
+    if (j < 4) {
+      sc = SB(j) & 63;
+      m = SB(j + 4) & 63;
+    } else {
+      sc = (SB(j + 4) & 0xF) | ((SB(j - 4) >> 6) << 4);
+      m = (SB(j + 4) >> 4) | ((SB(j) >> 6) << 4);
+    }
+    s[j] = d * (float)sc;
+    mb[j] = dmin * (float)m;
+  }
+#undef SB
+}
+
+// Dequantize half H (K 128*H .. 128*H+127) of one row's superblock into TMEM
+// A stage (2*unit + H) % kAStages.
+template <int H>
+SW_DEVICE bool dq_half(const uint4 (&q)[8], const float* sc, const float* mb, int unit,
+                       uint32_t tmem_lane_base, uint64_t* a_empty, uint64_t* a_full, int lane,
+                       int* status) {
+  const int j = 2 * unit + H, as = j % kAStages;
+  if (!mbar_wait(&a_empty[as], ((j / kAStages) & 1) ^ 1, status, 32)) return false;
+  tc_fence_after();
+  const uint32_t taddr = tmem_lane_base + kAColBase + as * 64;
+  const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
+#pragma unroll
+  for (int sbk = 0; sbk < 4; ++sbk) {
+    const int sub = 4 * H + sbk;
+    const __half2 S = __float2half2_rn(sc[sub]), S16 = __float2half2_rn(sc[sub] * 0.0625f);
+    const __half2 MB = __float2half2_rn(-mb[sub]);
+    uint32_t cols[16];
+#pragma unroll
+    for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[16 * H + 4 * sbk + w4], S, S16, MB, cols + 4 * w4);
+    tmem_st_x16(taddr + sbk * 16, cols);
+  }
+  tmem_wait_st();
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&a_full[as]);
+  return true;
+}
+
+template <int N>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    qgemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap x_map, QGemmArgs a) {
+  using C = QCfg<N>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* x_smem = smem;
+  uint8_t* w_smem = smem + C::X_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(w_smem + C::W_BYTES);
+  uint64_t* w_full = bars;
+  uint64_t* w_empty = w_full + C::W_ST;
+  uint64_t* x_full = w_empty + C::W_ST;
+  uint64_t* x_empty = x_full + C::X_ST;
+  uint64_t* a_full = x_empty + C::X_ST;
+  uint64_t* a_empty = a_full + kAStages;
+  uint64_t* d_full = a_empty + kAStages;
+  uint64_t* d_empty = d_full + 1;
+  uint64_t* done_bar = d_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long u0 = (long)blockIdx.x * a.upc;
+  const long u1 = min(a.total_units, u0 + a.upc);
+  const int n_units = (int)max(0L, u1 - u0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::W_ST; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
+    for (int i = 0; i < C::X_ST; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
+    for (int i = 0; i < kAStages; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+    mbar_init(d_full, 1);
+    mbar_init(d_empty, 4);
+    mbar_init(done_bar, 1);
+    fence_barrier_init();
+    prefetch_tensormap(&x_map);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued_w = 0, issued_x = 0;
+      bool ok = true;
+      for (int i = 0; i < n_units && ok; ++i) {
+        const long u = u0 + i;
+        const int tile = (int)(u / a.ksb), sb = (int)(u - (long)tile * a.ksb);
+        const int rt = tile / a.n_tok_tiles, nt = tile - rt * a.n_tok_tiles;
+        const int wsi = i % C::W_ST;
+        if (!(ok = mbar_wait(&w_empty[wsi], ((i / C::W_ST) & 1) ^ 1, a.status, 11))) break;
+        mbar_arrive_expect_tx(&w_full[wsi], kWStageBytes);
+        bulk_load(w_smem + wsi * kWStageBytes,
+                  a.w + ((size_t)rt * a.ksb + sb) * kWStageBytes, kWStageBytes, &w_full[wsi]);
+        ++issued_w;
+        for (int h = 0; h < 2; ++h) {
+          const int j = 2 * i + h, xs = j % C::X_ST;
+          if (!(ok = mbar_wait(&x_empty[xs], ((j / C::X_ST) & 1) ^ 1, a.status, 12))) break;
+          mbar_arrive_expect_tx(&x_full[xs], C::X_HALF_BYTES);
+          uint8_t* dst = x_smem + xs * C::X_HALF_BYTES;
+          const int k0 = sb * 256 + h * 128;
+          tma_load_2d(dst, &x_map, k0, nt * N, &x_full[xs]);
+          tma_load_2d(dst + N * 128, &x_map, k0 + 64, nt * N, &x_full[xs]);
+          ++issued_x;
+        }
+      }
+      if (!ok) {
+        // Drain our own copies still in flight before the CTA exits.
+        for (int i = max(0, issued_w - C::W_ST); i < issued_w; ++i)
+          mbar_wait(&w_full[i % C::W_ST], (i / C::W_ST) & 1, nullptr, 0);
+        for (int j = max(0, issued_x - C::X_ST); j < issued_x; ++j)
+          mbar_wait(&x_full[j % C::X_ST], (j / C::X_ST) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(128, N, /*f16*/ 0);
+      int seg = 0;
+      bool ok = true;
+      for (int i = 0; i < n_units && ok; ++i) {
+        const long u = u0 + i;
+        const int sb = (int)(u % a.ksb);
+        const bool first = (i == 0) || (sb == 0);
+        const bool last = (i == n_units - 1) || (sb == a.ksb - 1);
+        if (first && seg > 0) {
+          if (!(ok = mbar_wait(d_empty, (seg - 1) & 1, a.status, 21))) break;
+          tc_fence_after();
+        }
+        for (int h = 0; h < 2; ++h) {
+          const int j = 2 * i + h, as = j % kAStages, xs = j % C::X_ST;
+          if (!(ok = mbar_wait(&a_full[as], (j / kAStages) & 1, a.status, 22))) break;
+          if (!(ok = mbar_wait(&x_full[xs], (j / C::X_ST) & 1, a.status, 23))) break;
+          tc_fence_after();
+          const uint32_t xb = smem_u32(x_smem + xs * C::X_HALF_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t a_t = tmem_base + kAColBase + as * 64 + kk * 8;
+            const uint64_t bd =
+                smem_desc(xb + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024, /*sw128*/ 2);
+            umma_f16_ts(tmem_base, a_t, bd, idesc, (first && h == 0 && kk == 0) ? 0u : 1u);
+          }
+          umma_commit(&a_empty[as]);
+          umma_commit(&x_empty[xs]);
+        }
+        if (!ok) break;
+        if (last) {
+          umma_commit(d_full);
+          ++seg;
+        }
+      }
+      // All MMAs issued by this thread have completed once done_bar flips.
+      umma_commit(done_bar);
+      mbar_wait(done_bar, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant + epilogue
+    const int g = (warp - 2) >> 2;      // warpgroup
+    const int quad = warp & 3;          // TMEM lane quadrant this warp may touch
+    const int row = quad * 32 + lane;   // weight row inside the 128-row tile
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    int seg = 0;
+    bool ok = true;
+    for (int i = 0; i < n_units && ok; ++i) {
+      const long u = u0 + i;
+      const int tile = (int)(u / a.ksb), sb = (int)(u - (long)tile * a.ksb);
+      const bool last = (i == n_units - 1) || (sb == a.ksb - 1);
+      if ((i % kDqWG) == g) {
+        const int wsi = i % C::W_ST;
+        if (!(ok = mbar_wait(&w_full[wsi], (i / C::W_ST) & 1, a.status, 31))) break;
+        const uint4* src = reinterpret_cast<const uint4*>(w_smem + wsi * kWStageBytes +
+                                                           row * kQ4kRowBytes);
+        uint4 q[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) q[c] = src[c];
+        const uint4 hdr = src[8];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&w_empty[wsi]);
+        float sc_f[8], mb_f[8];
+        q4k_decode_scales(hdr, sc_f, mb_f);
+        ok = dq_half<0>(q, sc_f, mb_f, i, tmem_base + lane_off, a_empty, a_full, lane, a.status) &&
+             dq_half<1>(q, sc_f, mb_f, i, tmem_base + lane_off, a_empty, a_full, lane, a.status);
+        if (!ok) break;
+      }
+      if (last) {
+        if ((i % kDqWG) == g) {
+          // Drain the accumulator of this tile segment into workspace slot (tile + cta).
+          if (!(ok = mbar_wait(d_full, seg & 1, a.status, 33))) break;
+          tc_fence_after();
+          const int nt = tile % a.n_tok_tiles;
+          const int n_valid = min(N, a.T - nt * N);
+          float* dst = a.ws + ((size_t)(tile + blockIdx.x) * N) * 128 + row;
+#pragma unroll 1
+          for (int c = 0; c < N / 16; ++c) {
+            uint32_t r[16];
+            tmem_ld_x16(tmem_base + lane_off + c * 16, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              if (c * 16 + e < n_valid) dst[(size_t)(c * 16 + e) * 128] = __uint_as_float(r[e]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(d_empty);
+        }
+        ++seg;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// GGUF Q4_K [rows][K/256 blocks] -> tiled, nibble-permuted layout
+// [rows_pad/128][K/256][128][144].  Padding rows are zero.
+__global__ void q4k_repack_kernel(const uint8_t* __restrict__ src, int rows, int rows_pad, int K,
+                                  uint8_t* __restrict__ dst) {
+  const int ksb = K / 256;
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)rows_pad * ksb) return;
+  const int r = (int)(idx / ksb), sb = (int)(idx - (long)r * ksb);
+  uint8_t* out = dst + (((size_t)(r >> 7) * ksb + sb) * 128 + (r & 127)) * kQ4kRowBytes;
+  if (r >= rows) {
+    for (int i = 0; i < kQ4kRowBytes; ++i) out[i] = 0;
+    return;
+  }
+  const uint8_t* b = src + ((size_t)r * ksb + sb) * 144;
+  const uint8_t* qs = b + 16;
+  // Word w covers K [8w, 8w+8); nibble p holds k = 8w + perm[p], perm = 0,2,4,6,1,3,5,7.
+  for (int w = 0; w < 32; ++w) {
+    uint32_t word = 0;
+    for (int p = 0; p < 8; ++p) {
+      const int kk = 8 * w + ((p < 4) ? 2 * p : 2 * (p - 4) + 1);
+      const int g = kk >> 6, rr = kk & 63;
+      const uint8_t byte = qs[32 * g + (rr & 31)];
+      const uint32_t q = (rr < 32) ? (byte & 0xF) : (byte >> 4);
+      word |= q << (4 * p);
+    }
+    reinterpret_cast<uint32_t*>(out)[w] = word;
+  }
+  for (int i = 0; i < 16; ++i) out[128 + i] = b[i];
+}
+
+}  // namespace swarm
+
+using namespace swarm;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  }
+  return fn;
+}
+
+// 2D fp16/bf16 row-major tensor [rows, cols] (row stride in elements), box
+// {box_cols, box_rows}, 128 B swizzle when box_cols * 2 == 128.
+int make_tmap_2d_16bit(CUtensorMap* map, const void* base, int rows, int cols, int row_stride,
+                       int box_rows, int box_cols, int swizzle_bytes) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                          : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                   strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+int q4k_tc_tok_tile(int T) {
+  if (T <= 16) return 16;
+  if (T <= 32) return 32;
+  if (T <= 64) return 64;
+  if (T <= 128) return 128;
+  return 256;
+}
+
+// Work decomposition shared by the launcher, the workspace sizing and GemmOut.
+void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* ksb,
+                 long* total_units, int* upc, int* n_ctas, size_t* ws_floats) {
+  const int N = q4k_tc_tok_tile(T);
+  const int ntt = (T + N - 1) / N;
+  const int kb = K / 256;
+  const int tiles = ((rows + 127) / 128) * ntt;
+  const long total = (long)tiles * kb;
+  const int u = (int)((total + num_sms - 1) / num_sms);
+  const int ctas = (int)((total + u - 1) / u);
+  *tok_tile = N;
+  *n_tok_tiles = ntt;
+  *ksb = kb;
+  *total_units = total;
+  *upc = u;
+  *n_ctas = ctas;
+  *ws_floats = (size_t)(tiles + ctas) * N * 128;
+}
+
+template <int N>
+static int launch_n(const CUtensorMap& map, const QGemmArgs& a, int n_ctas, cudaStream_t s) {
+  using C = QCfg<N>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(qgemm_q4k_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM) != cudaSuccess)
+      return -3;
+    attr_set = true;
+  }
+  qgemm_q4k_tc_kernel<N><<<n_ctas, kGemmThreads, C::SMEM, s>>>(map, a);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, int x_stride,
+                        int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
+                        GemmOut* out, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (K % 256 != 0 || rows % 128 != 0) return -1;
+  if ((x_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return -5;
+  int N, ntt, kb, upc, ctas;
+  long total;
+  size_t need;
+  q4k_tc_plan(rows, K, T, num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need);
+  if (need > ws_floats_avail) return -6;
+  CUtensorMap map;
+  if (make_tmap_2d_16bit(&map, x, T, K, x_stride, N, 64, 128) != 0) return -2;
+  QGemmArgs a{(const uint8_t*)w_packed, rows, K, T, ntt, kb, total, upc, ws, status};
+  int rc;
+  switch (N) {
+    case 16: rc = launch_n<16>(map, a, ctas, s); break;
+    case 32: rc = launch_n<32>(map, a, ctas, s); break;
+    case 64: rc = launch_n<64>(map, a, ctas, s); break;
+    case 128: rc = launch_n<128>(map, a, ctas, s); break;
+    default: rc = launch_n<256>(map, a, ctas, s); break;
+  }
+  if (out) {
+    out->ws = ws;
+    out->rows = rows;
+    out->T = T;
+    out->mode = 1;
+    out->ksb = kb;
+    out->upc = upc;
+    out->tok_tile = N;
+    out->n_tok_tiles = ntt;
+    out->seg_max = 0;
+  }
+  return rc;
+}
+
+int launch_q4k_repack(const void* src, int rows, int K, void* dst, cudaStream_t s) {
+  const int rows_pad = (rows + 127) / 128 * 128;
+  const long n = (long)rows_pad * (K / 256);
+  q4k_repack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)src, rows,
+                                                                 rows_pad, K, (uint8_t*)dst);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}

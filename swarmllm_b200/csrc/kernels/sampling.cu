@@ -1,0 +1,235 @@
+// Token selection on the device: greedy argmax and temperature / top-k /
+// top-p sampling by the Gumbel-max trick with counter-based noise.
+//
+// The noise for (seed, position, token) comes from Philox4x32-10 (Salmon et
+// al., "Parallel Random Numbers: As Easy as 1, 2, 3", SC'11), so any rank or a
+// drafter that knows the seed and position redraws exactly the same Gumbel
+// variates: this is what makes coupled speculative sampling reproducible across
+// GPUs (the reference does the same on the host with Philox4x64-10,
+// src/inference/coupled_noise.rs:39,61).
+//
+// Top-k: the k-th largest logit is found by a 4-pass radix select over the
+// order-preserving integer image of the floats.  Top-p: the probability
+// threshold is found by bisection on the sorted-free "mass above tau" count.
+// Tokens below either threshold get no Gumbel draw.
+#include "kernels.h"
+#include "common.cuh"
+
+namespace swarm {
+
+SW_DEVICE uint32_t mulhilo(uint32_t a, uint32_t b, uint32_t& hi) {
+  hi = __umulhi(a, b);
+  return a * b;
+}
+
+// Philox4x32 with 10 rounds.
+SW_DEVICE uint4 philox4x32_10(uint4 ctr, uint2 key) {
+  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    uint32_t hi0, hi1;
+    uint32_t lo0 = mulhilo(M0, ctr.x, hi0);
+    uint32_t lo1 = mulhilo(M1, ctr.z, hi1);
+    ctr = make_uint4(hi1 ^ ctr.y ^ key.x, lo1, hi0 ^ ctr.w ^ key.y, lo0);
+    key.x += W0;
+    key.y += W1;
+  }
+  return ctr;
+}
+
+// Uniform in (0,1) for (seed, position, token).
+SW_DEVICE float philox_uniform(uint64_t seed, uint32_t position, uint32_t token) {
+  uint4 c = make_uint4(token, position, 0x5eedu, 0u);
+  uint2 k = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
+  uint4 r = philox4x32_10(c, k);
+  // 24 random bits -> (0,1), never 0 or 1.
+  return ((r.x >> 8) + 0.5f) * (1.0f / 16777216.0f);
+}
+
+SW_DEVICE uint32_t float_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+struct ArgMax {
+  float v;
+  int i;
+};
+
+SW_DEVICE ArgMax argmax_merge(ArgMax a, ArgMax b) {
+  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+  return a;
+}
+
+SW_DEVICE ArgMax block_argmax(ArgMax x, float* sv, int* si) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgMax y{__shfl_xor_sync(0xffffffffu, x.v, o), __shfl_xor_sync(0xffffffffu, x.i, o)};
+    x = argmax_merge(x, y);
+  }
+  __syncthreads();
+  if (lane == 0) { sv[wid] = x.v; si[wid] = x.i; }
+  __syncthreads();
+  if (wid == 0) {
+    ArgMax y = (lane < nw) ? ArgMax{sv[lane], si[lane]} : ArgMax{-INFINITY, 0x7fffffff};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ArgMax z{__shfl_xor_sync(0xffffffffu, y.v, o), __shfl_xor_sync(0xffffffffu, y.i, o)};
+      y = argmax_merge(y, z);
+    }
+    if (lane == 0) { sv[0] = y.v; si[0] = y.i; }
+  }
+  __syncthreads();
+  return ArgMax{sv[0], si[0]};
+}
+
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V,
+                                                      int stride, int32_t* __restrict__ out,
+                                                      float* __restrict__ out_val) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const float* row = logits + (size_t)blockIdx.x * stride;
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) best = argmax_merge(best, ArgMax{row[i], i});
+  best = block_argmax(best, sv, si);
+  if (threadIdx.x == 0) {
+    out[blockIdx.x] = best.i;
+    if (out_val) out_val[blockIdx.x] = best.v;
+  }
+}
+
+// Per row params: temperature (<=0 -> greedy), top_k (<=0 -> off), top_p (>=1 -> off).
+__global__ void __launch_bounds__(1024) sample_kernel(
+    const float* __restrict__ logits, int V, int stride, const float* __restrict__ temperature,
+    const int32_t* __restrict__ top_k, const float* __restrict__ top_p,
+    const uint64_t* __restrict__ seeds, const int32_t* __restrict__ positions,
+    int32_t* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t prefix_s, want_s;
+  __shared__ float red[32];
+  const int r = blockIdx.x;
+  const float* row = logits + (size_t)r * stride;
+  const float temp = temperature[r];
+  ArgMax best{-INFINITY, 0x7fffffff};
+  if (!(temp > 0.f)) {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) best = argmax_merge(best, ArgMax{row[i], i});
+    best = block_argmax(best, sv, si);
+    if (threadIdx.x == 0) out[r] = best.i;
+    return;
+  }
+  const float inv_t = 1.f / temp;
+  // Max logit (for the softmax used by top-p).
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, row[i]);
+  mx = block_max(mx, red);
+  // --- top-k threshold (k-th largest key) by radix select ------------------
+  uint32_t kth_key = 0;  // keep keys >= kth_key
+  const int k = top_k ? top_k[r] : 0;
+  if (k > 0 && k < V) {
+    if (threadIdx.x == 0) { prefix_s = 0; want_s = (uint32_t)k; }
+    uint32_t mask = 0;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+      __syncthreads();
+      const uint32_t prefix = prefix_s;
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        uint32_t key = float_key(row[i]);
+        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        uint32_t want = want_s, acc = 0;
+        int b = 255;
+        for (; b > 0; --b) {
+          if (acc + hist[b] >= want) break;
+          acc += hist[b];
+        }
+        want_s = want - acc;
+        prefix_s = prefix | ((uint32_t)b << shift);
+      }
+      mask |= 255u << shift;
+      __syncthreads();
+    }
+    kth_key = prefix_s;
+  }
+  // --- top-p threshold on probabilities by bisection -----------------------
+  float p_lo = 0.f;  // keep tokens with prob >= p_lo
+  const float tp = top_p ? top_p[r] : 1.f;
+  if (tp < 1.f) {
+    float z = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+      if (float_key(row[i]) >= kth_key) z += __expf((row[i] - mx) * inv_t);
+    z = block_sum(z, red);
+    float lo = 0.f, hi = 1.f;  // probability thresholds
+    for (int it = 0; it < 24; ++it) {
+      const float mid = 0.5f * (lo + hi);
+      float m = 0.f;
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        if (float_key(row[i]) < kth_key) continue;
+        float p = __expf((row[i] - mx) * inv_t) / z;
+        if (p >= mid) m += p;
+      }
+      m = block_sum(m, red);
+      if (m >= tp) lo = mid; else hi = mid;
+    }
+    p_lo = lo;
+  }
+  const uint64_t seed = seeds ? seeds[r] : 0ull;
+  const uint32_t pos = positions ? (uint32_t)positions[r] : 0u;
+  float z = 1.f;
+  if (p_lo > 0.f) {
+    float zz = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x)
+      if (float_key(row[i]) >= kth_key) zz += __expf((row[i] - mx) * inv_t);
+    z = block_sum(zz, red);
+  }
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float l = row[i];
+    if (float_key(l) < kth_key) continue;
+    if (p_lo > 0.f && __expf((l - mx) * inv_t) / z < p_lo) continue;
+    const float u = philox_uniform(seed, pos, (uint32_t)i);
+    const float g = -logf(-logf(u));
+    best = argmax_merge(best, ArgMax{(l - mx) * inv_t + g, i});
+  }
+  best = block_argmax(best, sv, si);
+  if (threadIdx.x == 0) out[r] = best.i;
+}
+
+__global__ void philox_uniform_kernel(uint64_t seed, const int32_t* positions, int n_pos, int V,
+                                      float* out) {
+  const int r = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x)
+    out[(size_t)r * V + i] = philox_uniform(seed, (uint32_t)positions[r], (uint32_t)i);
+}
+
+}  // namespace swarm
+
+using namespace swarm;
+
+void launch_argmax(const float* logits, int rows, int V, int stride, int32_t* out, float* out_val,
+                   cudaStream_t s) {
+  if (rows <= 0) return;
+  argmax_kernel<<<rows, 1024, 0, s>>>(logits, V, stride, out, out_val);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_sample(const float* logits, int rows, int V, int stride, const float* temperature,
+                   const int32_t* top_k, const float* top_p, const uint64_t* seeds,
+                   const int32_t* positions, int32_t* out, cudaStream_t s) {
+  if (rows <= 0) return;
+  sample_kernel<<<rows, 1024, 0, s>>>(logits, V, stride, temperature, top_k, top_p, seeds,
+                                      positions, out);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_philox_uniform(uint64_t seed, const int32_t* positions, int n_pos, int V, float* out,
+                           cudaStream_t s) {
+  if (n_pos <= 0) return;
+  dim3 grid((V + 255) / 256 < 512 ? (V + 255) / 256 : 512, n_pos);
+  philox_uniform_kernel<<<grid, 256, 0, s>>>(seed, positions, n_pos, V, out);
+  SW_LAUNCH_CHECK();
+}

@@ -1,0 +1,194 @@
+"""LLMEngine: the public single-process inference API.
+
+    eng = LLMEngine.from_config(preset("llama-3.2-3b"), device="cuda:0")
+    outs = eng.generate([[1, 2, 3]], SamplingParams(max_tokens=32))
+
+One engine owns: the C++ BlockManager (paged KV pages + prefix cache), the
+C++ Scheduler (continuous batching, chunked prefill, preemption), a runner
+(GPU with CUDA graphs, or CPU) and per-request sampling parameters.  Each
+``step()`` = schedule -> one forward over the mixed batch -> token selection
+-> commit.  Finished requests are reported with their tokens and timings.
+Reference: the worker's run loop (src/inference/model_worker.rs:173,11934)
+plus ModelProcessPool::generate (src/inference/process_pool.rs:14208).
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from ..models.config import ModelConfig
+from ..ops.attention import PagedKVCache
+from ..utils.ext import native
+from ..utils.tracing import RequestTrace, StageProfiler
+from .runner import CpuRunner, GpuRunner
+from .sampling import SamplingParams
+
+
+@dataclass
+class EngineConfig:
+    max_model_len: int = 4096
+    max_step_tokens: int = 2048     # per-step token budget (prefill chunk + decodes)
+    max_running: int = 64           # max concurrent sequences
+    prefill_chunk: int = 2048       # reference default is 128 (config/default.toml); B200 affords more
+    page_size: int = 16
+    kv_pages: int = 0               # 0 -> derive from kv_fraction of free memory
+    kv_fraction: float = 0.85       # reference VRAM_HEADROOM_PCT = 85 (split/kv_budget.rs:58)
+    prefix_cache: bool = True
+    cuda_graphs: bool = True
+    graph_sizes: tuple = (1, 2, 4, 8, 16, 32, 64)
+
+
+@dataclass
+class RequestOutput:
+    request_id: int
+    prompt_len: int
+    token_ids: list
+    finished: bool
+    trace: RequestTrace | None = None
+
+
+class LLMEngine:
+    def __init__(self, model, cfg: ModelConfig, ecfg: EngineConfig, device="cuda:0"):
+        self.cfg, self.ecfg = cfg, ecfg
+        self.device = torch.device(device)
+        self.model = model
+        N = native()
+        ps = ecfg.page_size
+        if self.device.type == "cuda":
+            pages = ecfg.kv_pages or self._auto_pages()
+            # one extra page: the trash page that graph padding rows write to
+            self.kv = PagedKVCache(model.hi - model.lo, pages + 1, cfg.n_kv_heads, cfg.head_dim,
+                                   self.device, ps)
+            self.bm = N.BlockManager(pages, ps, ecfg.prefix_cache)
+            self.runner = GpuRunner(model, self.kv, ecfg.max_step_tokens, ecfg.max_running,
+                                    ecfg.max_model_len, ecfg.graph_sizes, ecfg.cuda_graphs,
+                                    trash_page=pages)
+            if ecfg.cuda_graphs:
+                self.runner.capture_graphs()
+        else:
+            pages = ecfg.kv_pages or (ecfg.max_running * ((ecfg.max_model_len + ps - 1) // ps))
+            nl = model.hi - model.lo
+            self.kv = PagedKVCache(nl, pages, cfg.n_kv_heads, cfg.head_dim, "cpu", ps,
+                                   dtype=torch.float32)
+            self.bm = N.BlockManager(pages, ps, ecfg.prefix_cache)
+            self.runner = CpuRunner(model, self.kv, ecfg.max_model_len)
+        self.sched = N.Scheduler(self.bm, ecfg.max_step_tokens, ecfg.max_running, ecfg.prefill_chunk)
+        self.params: dict[int, SamplingParams] = {}
+        self.traces: dict[int, RequestTrace] = {}
+        self.prompt_len: dict[int, int] = {}
+        self._ids = itertools.count()
+        self.profiler = StageProfiler()
+        self.steps = 0
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def from_config(cls, cfg: ModelConfig, device="cuda:0", ecfg: EngineConfig | None = None,
+                    source=None, seed: int = 0):
+        from ..models.llama import LlamaCPU, LlamaGPU
+        from ..models.weights import RandomSource
+        ecfg = ecfg or EngineConfig()
+        dev = torch.device(device)
+        if source is None:
+            source = RandomSource(cfg, seed=seed, on_device=dev.type == "cuda")
+        if dev.type == "cuda":
+            model = LlamaGPU(cfg, source, dev)
+        else:
+            model = LlamaCPU(cfg, source)
+        return cls(model, cfg, ecfg, dev)
+
+    @classmethod
+    def from_gguf(cls, path: str, device="cuda:0", ecfg: EngineConfig | None = None):
+        from ..models.weights import GgufSource
+        src = GgufSource(path)
+        return cls.from_config(src.cfg, device, ecfg, source=src)
+
+    def _auto_pages(self) -> int:
+        free, _ = torch.cuda.mem_get_info(self.device)
+        per_page = PagedKVCache.bytes_per_page(self.model.hi - self.model.lo, self.cfg.n_kv_heads,
+                                               self.cfg.head_dim, self.ecfg.page_size)
+        # leave room for activations / workspaces
+        budget = free * self.ecfg.kv_fraction - 4 * (1 << 30)
+        need = self.ecfg.max_running * ((self.ecfg.max_model_len + self.ecfg.page_size - 1)
+                                        // self.ecfg.page_size)
+        return int(max(64, min(budget // per_page, need)))
+
+    # ------------------------------------------------------------------ API
+    def add_request(self, prompt_ids, params: SamplingParams | None = None,
+                    request_id: int | None = None) -> int:
+        params = params or SamplingParams()
+        rid = next(self._ids) if request_id is None else request_id
+        eos = -1 if params.ignore_eos else params.eos_token_id
+        self.sched.add_request(rid, [int(t) for t in prompt_ids], int(params.max_tokens), int(eos))
+        self.params[rid] = params
+        self.prompt_len[rid] = len(prompt_ids)
+        self.traces[rid] = RequestTrace(rid, len(prompt_ids))
+        return rid
+
+    def abort(self, rid: int):
+        self.sched.abort(rid)
+
+    def has_work(self) -> bool:
+        return self.sched.has_work()
+
+    def step(self) -> list[tuple[int, int, bool]]:
+        """One engine iteration.  Returns (request_id, new_token, finished) for
+        every request that produced a token."""
+        plan = self.sched.schedule()
+        if len(plan) == 0:
+            return []
+        ids = [int(s) for s in plan.seq_ids]
+        samp = plan.seq_sample
+        params = [self.params[i] for i, s in zip(ids, samp) if s]
+        with self.profiler.stage("forward"):
+            sampled = self.runner.run(plan, self.bm, params)
+        done = set(int(d) for d in self.sched.commit(plan, sampled.tolist()))
+        out = []
+        now = time.perf_counter()
+        k = 0
+        for i, s in zip(ids, samp):
+            if not s:
+                continue
+            tok = int(sampled[k])
+            k += 1
+            tr = self.traces.get(i)
+            if tr is not None:
+                tr.on_token(now)
+            out.append((i, tok, i in done))
+        self.steps += 1
+        return out
+
+    def output(self, rid: int) -> list[int]:
+        return [int(t) for t in self.sched.output(rid)]
+
+    def release(self, rid: int):
+        self.sched.release(rid)
+        self.params.pop(rid, None)
+        self.prompt_len.pop(rid, None)
+
+    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None
+                 ) -> list[RequestOutput]:
+        if not isinstance(params, list):
+            params = [params or SamplingParams()] * len(prompts)
+        rids = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
+        pending = set(rids)
+        results: dict[int, list[int]] = {r: [] for r in rids}
+        while pending:
+            for rid, tok, fin in self.step():
+                if rid in results:
+                    results[rid].append(tok)
+                if fin:
+                    pending.discard(rid)
+            if not self.sched.has_work() and pending:
+                raise RuntimeError("scheduler idle with pending requests")
+        outs = []
+        for r in rids:
+            tr = self.traces.pop(r, None)
+            if tr:
+                tr.finish(time.perf_counter())
+            outs.append(RequestOutput(r, self.prompt_len[r], results[r], True, tr))
+            self.release(r)
+        return outs

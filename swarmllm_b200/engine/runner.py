@@ -1,0 +1,181 @@
+"""Model runners: turn a scheduler StepPlan into one forward + token selection.
+
+``GpuRunner`` (one GPU):
+  * host side builds the per-row arrays (tokens, positions, KV slots,
+    block-table rows, visible lengths, sampled rows) into pinned buffers and
+    copies them to static device buffers with one async H2D each;
+  * decode-only steps whose batch fits a captured size replay a CUDA graph of
+    the whole forward (the reference's central finding is that decode is bound
+    by launch count: 1,085 submissions per token, docs/invariants/inference.md:1727;
+    its graphs cover 2-layer groups, src/inference/cuda_graph.rs:274 -- here the
+    graph covers the entire step);
+  * token selection runs on the device; only the sampled ids come back (D2H).
+
+``CpuRunner`` runs the fp32 CPU model with the same interface.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from ..models.llama import StepBatch
+from ..ops.attention import PagedKVCache
+from .sampling import DeviceSampler, SamplingParams, sample_host
+
+
+def plan_arrays(plan, block_manager, max_pages: int):
+    """numpy per-row arrays of a StepPlan."""
+    tokens = plan.tokens
+    positions = plan.positions
+    slots = plan.slots
+    row_seq = plan.row_seq
+    seq_ids = [int(s) for s in plan.seq_ids]
+    bt_seq = block_manager.block_table(seq_ids, max_pages) if seq_ids else np.zeros((0, max_pages), np.int32)
+    bt_rows = bt_seq[row_seq] if len(row_seq) else np.zeros((0, max_pages), np.int32)
+    seq_lens = (positions + 1).astype(np.int32)
+    start, ntok, samp = plan.seq_start, plan.seq_ntok, plan.seq_sample
+    sample_rows = np.array([start[b] + ntok[b] - 1 for b in range(len(seq_ids)) if samp[b]],
+                           dtype=np.int64)
+    return tokens, positions, slots, bt_rows, seq_lens, sample_rows
+
+
+class GpuRunner:
+    def __init__(self, model, kv: PagedKVCache, max_tokens: int, max_seqs: int, max_model_len: int,
+                 graph_sizes=(1, 2, 4, 8, 16, 32, 64), use_graphs: bool = True, trash_page: int = -1):
+        self.model, self.kv = model, kv
+        self.device = model.device
+        self.max_tokens, self.max_seqs = max_tokens, max_seqs
+        self.max_model_len = max_model_len
+        self.max_pages = (max_model_len + kv.page_size - 1) // kv.page_size
+        self.ctx = model.make_context(max_tokens, max(max_seqs, max(graph_sizes)), max_model_len)
+        self.sampler = DeviceSampler(self.device, max(max_seqs, max(graph_sizes)))
+        dev = self.device
+        mt = max_tokens
+        # static device inputs (graph-safe addresses)
+        self.d_tokens = torch.zeros(mt, dtype=torch.int32, device=dev)
+        self.d_pos = torch.zeros(mt, dtype=torch.int32, device=dev)
+        self.d_slots = torch.zeros(mt, dtype=torch.int32, device=dev)
+        self.d_bt = torch.zeros(mt, self.max_pages, dtype=torch.int32, device=dev)
+        self.d_lens = torch.ones(mt, dtype=torch.int32, device=dev)
+        self.d_samp = torch.zeros(mt, dtype=torch.int64, device=dev)
+        # pinned host staging
+        self.h_i32 = torch.zeros(4 * mt, dtype=torch.int32).pin_memory()
+        self.h_bt = torch.zeros(mt, self.max_pages, dtype=torch.int32).pin_memory()
+        self.h_samp = torch.zeros(mt, dtype=torch.int64).pin_memory()
+        self.h_out = torch.zeros(mt, dtype=torch.int32).pin_memory()
+        self.trash_page = trash_page if trash_page >= 0 else kv.num_pages - 1
+        self.graph_sizes = sorted(s for s in graph_sizes if s <= min(max_tokens, max_seqs))
+        self.use_graphs = use_graphs
+        self.graphs: dict[int, tuple] = {}
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.launches_per_step = None
+
+    # ------------------------------------------------------------------ inputs
+    def _upload(self, tokens, positions, slots, bt_rows, seq_lens, sample_rows, pad_to: int = 0):
+        N = len(tokens)
+        M = max(N, pad_to)
+        h = self.h_i32
+        mt0 = self.max_tokens
+        h[0:N] = torch.from_numpy(np.asarray(tokens, np.int32))
+        h[mt0: mt0 + N] = torch.from_numpy(np.asarray(positions, np.int32))
+        h[2 * mt0: 2 * mt0 + N] = torch.from_numpy(np.asarray(slots, np.int32))
+        h[3 * mt0: 3 * mt0 + N] = torch.from_numpy(np.asarray(seq_lens, np.int32))
+        self.h_bt[:N] = torch.from_numpy(bt_rows)
+        S = len(sample_rows)
+        self.h_samp[:S] = torch.from_numpy(sample_rows)
+        if M > N:  # padding rows write to the trash page and read one key from it
+            h[N:M] = 0
+            h[mt0 + N: mt0 + M] = 0
+            h[2 * mt0 + N: 2 * mt0 + M] = self.trash_page * self.kv.page_size
+            h[3 * mt0 + N: 3 * mt0 + M] = 1
+            self.h_bt[N:M] = self.trash_page
+            self.h_samp[S:M] = torch.arange(S, M, dtype=torch.int64) if S < M else 0
+        self.d_tokens[:M].copy_(h[0:M], non_blocking=True)
+        self.d_pos[:M].copy_(h[mt0:mt0 + M], non_blocking=True)
+        self.d_slots[:M].copy_(h[2 * mt0:2 * mt0 + M], non_blocking=True)
+        self.d_lens[:M].copy_(h[3 * mt0:3 * mt0 + M], non_blocking=True)
+        self.d_bt[:M].copy_(self.h_bt[:M], non_blocking=True)
+        Sm = max(S, pad_to)
+        self.d_samp[:Sm].copy_(self.h_samp[:Sm], non_blocking=True)
+        self.h2d_bytes = 4 * 4 * M + 4 * M * self.max_pages + 8 * Sm
+        return M, Sm
+
+    def _batch(self, M: int, S: int) -> StepBatch:
+        return StepBatch(self.d_tokens[:M], self.d_pos[:M], self.d_slots[:M], self.d_bt[:M],
+                         self.d_lens[:M], self.d_samp[:S], self.max_model_len)
+
+    # ------------------------------------------------------------------ graphs
+    def capture_graphs(self):
+        if not self.use_graphs:
+            return
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for B in self.graph_sizes:
+                b = self._batch(B, B)
+                self._init_dummy(B)
+                for _ in range(2):  # warm up (sets kernel attributes, tensor maps)
+                    self.model.forward(b, self.kv, self.ctx)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    logits = self.model.forward(b, self.kv, self.ctx)
+                    out = self.sampler.greedy(logits)
+                self.graphs[B] = (g, logits, out)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+
+    def _init_dummy(self, B: int):
+        self.d_tokens[:B] = 0
+        self.d_pos[:B] = 0
+        self.d_slots[:B] = self.trash_page * self.kv.page_size
+        self.d_lens[:B] = 1
+        self.d_bt[:B] = self.trash_page
+        self.d_samp[:B] = torch.arange(B, device=self.device)
+
+    # ------------------------------------------------------------------ step
+    def run(self, plan, block_manager, params: list[SamplingParams]) -> np.ndarray:
+        tokens, positions, slots, bt_rows, seq_lens, sample_rows = plan_arrays(
+            plan, block_manager, self.max_pages)
+        N, S = len(tokens), len(sample_rows)
+        if N == 0:
+            return np.zeros(0, np.int32)
+        decode_only = plan.n_prefill_tokens == 0 and N == S
+        greedy = all(p.greedy for p in params)
+        B = next((b for b in self.graph_sizes if b >= N), None) if decode_only else None
+        if B is not None and B in self.graphs and greedy:
+            self._upload(tokens, positions, slots, bt_rows, seq_lens, sample_rows, pad_to=B)
+            g, logits, out = self.graphs[B]
+            g.replay()
+            res = out[:S]
+        else:
+            M, _ = self._upload(tokens, positions, slots, bt_rows, seq_lens, sample_rows)
+            logits = self.model.forward(self._batch(M, S), self.kv, self.ctx)
+            res = self.sampler.sample(logits, params, positions[sample_rows] if S else [])
+        self.h_out[:S].copy_(res, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        self.d2h_bytes = 4 * S
+        return self.h_out[:S].numpy().copy()
+
+
+class CpuRunner:
+    def __init__(self, model, kv: PagedKVCache, max_model_len: int):
+        self.model, self.kv = model, kv
+        self.max_model_len = max_model_len
+        self.max_pages = (max_model_len + kv.page_size - 1) // kv.page_size
+
+    def forward_plan(self, plan, block_manager, h_in=None):
+        tokens, positions, slots, bt_rows, seq_lens, sample_rows = plan_arrays(
+            plan, block_manager, self.max_pages)
+        b = StepBatch(torch.from_numpy(np.asarray(tokens, np.int32)),
+                      torch.from_numpy(np.asarray(positions, np.int32)),
+                      torch.from_numpy(np.asarray(slots, np.int32)), torch.from_numpy(bt_rows),
+                      torch.from_numpy(seq_lens), torch.from_numpy(sample_rows), self.max_model_len)
+        return self.model.forward(b, self.kv, None, h_in), positions, sample_rows
+
+    def run(self, plan, block_manager, params: list[SamplingParams]) -> np.ndarray:
+        if len(plan) == 0:
+            return np.zeros(0, np.int32)
+        logits, positions, sample_rows = self.forward_plan(plan, block_manager)
+        self.last_logits = logits
+        return sample_host(logits, params, positions[sample_rows])

@@ -1,0 +1,118 @@
+"""Sampling parameters and token selection.
+
+Greedy and temperature/top-k/top-p sampling run on the device
+(``sampling.cu``); the CPU backend mirrors them with the same Philox noise
+definition so a CPU run and a GPU run with the same seed pick the same
+tokens up to logit rounding.  Reference: src/inference/sampling.rs:314,339.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ..utils.ext import C
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    temperature: float = 0.0     # <= 0 -> greedy
+    top_k: int = 0
+    top_p: float = 1.0
+    seed: int = 0
+    eos_token_id: int = -1
+    ignore_eos: bool = False
+
+    @property
+    def greedy(self) -> bool:
+        return self.temperature <= 0.0
+
+
+class DeviceSampler:
+    """Batched token selection for up to `max_rows` rows per step."""
+
+    def __init__(self, device, max_rows: int):
+        self.device = torch.device(device)
+        self.out = torch.zeros(max_rows, dtype=torch.int32, device=device)
+        self.temp = torch.zeros(max_rows, dtype=torch.float32, device=device)
+        self.top_k = torch.zeros(max_rows, dtype=torch.int32, device=device)
+        self.top_p = torch.ones(max_rows, dtype=torch.float32, device=device)
+        self.seeds = torch.zeros(max_rows, dtype=torch.int64, device=device)
+        self.pos = torch.zeros(max_rows, dtype=torch.int32, device=device)
+        self.h_params = torch.zeros(max_rows, 5, dtype=torch.float64).pin_memory()
+
+    def greedy(self, logits: torch.Tensor) -> torch.Tensor:
+        S = logits.shape[0]
+        out = self.out[:S]
+        C().argmax(logits, out, None)
+        return out
+
+    def sample(self, logits: torch.Tensor, params: list[SamplingParams], positions: np.ndarray) -> torch.Tensor:
+        S = logits.shape[0]
+        if all(p.greedy for p in params):
+            return self.greedy(logits)
+        t = torch.tensor([p.temperature for p in params], dtype=torch.float32)
+        k = torch.tensor([p.top_k for p in params], dtype=torch.int32)
+        pp = torch.tensor([p.top_p for p in params], dtype=torch.float32)
+        sd = torch.tensor([p.seed for p in params], dtype=torch.int64)
+        ps = torch.from_numpy(np.asarray(positions, dtype=np.int32))
+        self.temp[:S].copy_(t, non_blocking=True)
+        self.top_k[:S].copy_(k, non_blocking=True)
+        self.top_p[:S].copy_(pp, non_blocking=True)
+        self.seeds[:S].copy_(sd, non_blocking=True)
+        self.pos[:S].copy_(ps, non_blocking=True)
+        out = self.out[:S]
+        C().sample(logits, self.temp[:S], self.top_k[:S], self.top_p[:S], self.seeds[:S],
+                   self.pos[:S], out)
+        return out
+
+
+# --------------------------------------------------------------------------- host mirror
+def philox_uniform_host(seed: int, position: int, tokens: np.ndarray) -> np.ndarray:
+    """Philox4x32-10 uniforms, bit-identical to the device definition."""
+    M0, M1, W0, W1 = 0xD2511F53, 0xCD9E8D57, 0x9E3779B9, 0xBB67AE85
+    mask = 0xFFFFFFFF
+    tok = np.asarray(tokens, dtype=np.uint64)
+    c0 = tok.copy()
+    c1 = np.full_like(tok, position & mask)
+    c2 = np.full_like(tok, 0x5EED)
+    c3 = np.zeros_like(tok)
+    k0, k1 = seed & mask, (seed >> 32) & mask
+    for _ in range(10):
+        p0 = M0 * c0
+        p1 = M1 * c2
+        hi0, lo0 = (p0 >> 32) & mask, p0 & mask
+        hi1, lo1 = (p1 >> 32) & mask, p1 & mask
+        c0, c1, c2, c3 = (hi1 ^ c1 ^ k0) & mask, lo1, (hi0 ^ c3 ^ k1) & mask, lo0
+        k0, k1 = (k0 + W0) & mask, (k1 + W1) & mask
+    return (((c0 >> 8).astype(np.float64) + 0.5) / 16777216.0).astype(np.float32)
+
+
+def sample_host(logits: torch.Tensor, params: list[SamplingParams], positions) -> np.ndarray:
+    """CPU token selection with the same rules as the device kernel."""
+    out = np.zeros(logits.shape[0], dtype=np.int32)
+    L = logits.detach().to(torch.float32).cpu().numpy()
+    for r, p in enumerate(params):
+        row = L[r]
+        if p.greedy:
+            out[r] = int(np.argmax(row))
+            continue
+        z = (row - row.max()) / p.temperature
+        keep = np.ones_like(row, dtype=bool)
+        if 0 < p.top_k < row.size:
+            kth = np.partition(row, -p.top_k)[-p.top_k]
+            keep &= row >= kth
+        if p.top_p < 1.0:
+            pr = np.where(keep, np.exp(z), 0.0)
+            pr /= pr.sum()
+            order = np.argsort(-pr)
+            cum = np.cumsum(pr[order])
+            cut = np.searchsorted(cum, p.top_p) + 1
+            thr = pr[order[min(cut, len(order)) - 1]]
+            keep &= pr >= thr
+        u = philox_uniform_host(p.seed, int(positions[r]), np.arange(row.size))
+        g = -np.log(-np.log(u))
+        out[r] = int(np.argmax(np.where(keep, z + g, -np.inf)))
+    return out

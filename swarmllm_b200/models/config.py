@@ -1,0 +1,312 @@
+"""Model architecture configs, the benchmark presets, and GGUF metadata mapping.
+
+Families (reference: ``src/inference/model_arch.rs:7-67``, architecture
+mapping in ``src/inference/split/loader/mod.rs``):
+
+* ``llama``     dense decoder: GQA attention, SwiGLU FFN, RMSNorm, RoPE
+                (GGML "norm" interleaved pairs), optional llama3 / linear /
+                YaRN frequency scaling.
+* ``gpt-oss``   MoE decoder: attention with learned sinks and bias, sliding
+                window on alternate layers, YaRN RoPE (NEOX), top-k softmax
+                routed experts with clamped SwiGLU, MXFP4 experts.
+* ``qwen3next`` hybrid: gated DeltaNet linear-attention layers and gated full
+                attention layers (3:1), q/k RMSNorm, partial NEOX RoPE,
+                512-expert MoE with a shared expert.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass, field, replace
+
+import numpy as np
+
+
+@dataclass
+class ModelConfig:
+    name: str = "model"
+    arch: str = "llama"
+    n_layers: int = 2
+    hidden: int = 256
+    n_heads: int = 4
+    n_kv_heads: int = 2
+    head_dim: int = 64
+    ffn: int = 512
+    vocab: int = 32000
+    rope_theta: float = 10000.0
+    rope_scaling: dict | None = None    # {"type": "llama3"|"yarn"|"linear", ...}
+    rope_neox: bool = False             # False = GGML "norm" interleaved pairs
+    rope_dim: int = 0                   # 0 -> head_dim (partial rotary otherwise)
+    rms_eps: float = 1e-5
+    tie_embeddings: bool = False
+    attn_bias: bool = False
+    qk_norm: bool = False
+    attn_sinks: bool = False
+    sliding_window: int = 0
+    swa_every: int = 0                  # layer l uses SWA if swa_every and l % swa_every == 0
+    attn_output_gate: bool = False      # qwen3next gated attention
+    # MoE
+    n_experts: int = 0
+    n_experts_used: int = 0
+    expert_ffn: int = 0
+    shared_expert_ffn: int = 0
+    moe_softmax_after_topk: bool = True  # gpt-oss: softmax over the selected logits
+    swiglu_limit: float = 0.0           # gpt-oss clamped SwiGLU (7.0)
+    swiglu_alpha: float = 1.702
+    # hybrid linear attention (gated DeltaNet)
+    full_attn_interval: int = 0         # every Nth layer (1-based) is full attention
+    ssm_k_heads: int = 0
+    ssm_v_heads: int = 0
+    ssm_head_dim: int = 128
+    ssm_conv_kernel: int = 4
+    # storage types
+    weight_qtype: str = "Q4_K"
+    embed_qtype: str = "F16"
+    output_qtype: str = ""              # "" -> weight_qtype
+    expert_qtype: str = ""              # "" -> weight_qtype
+
+    @property
+    def q_dim(self) -> int:
+        return self.n_heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.n_kv_heads * self.head_dim
+
+    @property
+    def rot_dim(self) -> int:
+        return self.rope_dim or self.head_dim
+
+    def is_swa(self, layer: int) -> bool:
+        return bool(self.sliding_window and self.swa_every and layer % self.swa_every == 0)
+
+    def is_linear_attn(self, layer: int) -> bool:
+        return bool(self.full_attn_interval) and (layer + 1) % self.full_attn_interval != 0
+
+    def is_moe(self, layer: int) -> bool:
+        return self.n_experts > 0
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+    def scaled(self, **kw) -> "ModelConfig":
+        return replace(self, **kw)
+
+    def param_count(self) -> int:
+        h, L = self.hidden, self.n_layers
+        attn = h * (self.q_dim + 2 * self.kv_dim) + self.q_dim * h
+        if self.n_experts:
+            ffn = self.n_experts * 3 * h * self.expert_ffn + h * self.n_experts
+            ffn += 3 * h * self.shared_expert_ffn
+        else:
+            ffn = 3 * h * self.ffn
+        emb = self.vocab * h * (1 if self.tie_embeddings else 2)
+        return L * (attn + ffn) + emb
+
+
+def rope_inv_freq(cfg: ModelConfig) -> tuple[np.ndarray, float]:
+    """Per-pair inverse frequencies (length rot_dim/2) and the cos/sin
+    attention factor, including llama3 / linear / YaRN scaling.  The scaling
+    rules are the published ones (Meta's llama3 rope_scaling; YaRN, Peng et
+    al. 2023); the reference implements the same in src/inference/split/rope.rs:66-249."""
+    d = cfg.rot_dim
+    inv = 1.0 / (cfg.rope_theta ** (np.arange(0, d, 2, dtype=np.float64) / d))
+    factor_attn = 1.0
+    rs = cfg.rope_scaling or {}
+    t = rs.get("type")
+    if t == "linear":
+        inv = inv / rs["factor"]
+    elif t == "llama3":
+        factor = rs.get("factor", 8.0)
+        lo, hi = rs.get("low_freq_factor", 1.0), rs.get("high_freq_factor", 4.0)
+        old = rs.get("original_max_position_embeddings", 8192)
+        lo_wl, hi_wl = old / lo, old / hi
+        wl = 2 * math.pi / inv
+        smooth = (old / wl - lo) / (hi - lo)
+        scaled = np.where(wl > lo_wl, inv / factor, inv)
+        mid = (wl <= lo_wl) & (wl >= hi_wl)
+        scaled = np.where(mid, (1 - smooth) * inv / factor + smooth * inv, scaled)
+        inv = scaled
+    elif t == "yarn":
+        factor = rs.get("factor", 32.0)
+        old = rs.get("original_max_position_embeddings", 4096)
+        beta_fast, beta_slow = rs.get("beta_fast", 32.0), rs.get("beta_slow", 1.0)
+
+        def corr_dim(rot):
+            return d * math.log(old / (rot * 2 * math.pi)) / (2 * math.log(cfg.rope_theta))
+
+        low = max(math.floor(corr_dim(beta_fast)), 0)
+        high = min(math.ceil(corr_dim(beta_slow)), d - 1)
+        ramp = np.clip((np.arange(d // 2, dtype=np.float64) - low) / max(high - low, 1e-3), 0, 1)
+        extra = 1.0 - ramp  # 1 -> keep original (high frequency)
+        inv = inv / factor * (1 - extra) + inv * extra
+        factor_attn = 0.1 * math.log(factor) + 1.0
+    return inv.astype(np.float32), float(factor_attn)
+
+
+# --------------------------------------------------------------------------- presets
+def tiny_llama() -> ModelConfig:
+    """2 layers, hidden 256, 4/2 heads, d 64, FFN 512, Q4_0."""
+    return ModelConfig(name="tiny-llama", arch="llama", n_layers=2, hidden=256, n_heads=4,
+                       n_kv_heads=2, head_dim=64, ffn=512, vocab=32000, rope_theta=10000.0,
+                       rms_eps=1e-5, weight_qtype="Q4_0", embed_qtype="Q4_0",
+                       output_qtype="Q4_0")
+
+
+def llama32_3b() -> ModelConfig:
+    """Llama-3.2-3B architecture, Q4_K weights."""
+    return ModelConfig(name="llama-3.2-3b", arch="llama", n_layers=28, hidden=3072, n_heads=24,
+                       n_kv_heads=8, head_dim=128, ffn=8192, vocab=128256, rope_theta=500000.0,
+                       rope_scaling={"type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
+                                     "high_freq_factor": 4.0,
+                                     "original_max_position_embeddings": 8192},
+                       rms_eps=1e-5, tie_embeddings=True, weight_qtype="Q4_K", embed_qtype="F16",
+                       output_qtype="Q4_K")
+
+
+def llama32_1b() -> ModelConfig:
+    """Drafter for config 3: Llama-3.2-1B architecture."""
+    return ModelConfig(name="llama-3.2-1b", arch="llama", n_layers=16, hidden=2048, n_heads=32,
+                       n_kv_heads=8, head_dim=64, ffn=8192, vocab=128256, rope_theta=500000.0,
+                       rope_scaling={"type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
+                                     "high_freq_factor": 4.0,
+                                     "original_max_position_embeddings": 8192},
+                       rms_eps=1e-5, tie_embeddings=True, weight_qtype="Q4_K", embed_qtype="F16",
+                       output_qtype="Q4_K")
+
+
+def llama33_70b() -> ModelConfig:
+    """BASELINE config 3 / the headline: Llama-3.3-70B architecture, Q4_K."""
+    return ModelConfig(name="llama-3.3-70b", arch="llama", n_layers=80, hidden=8192, n_heads=64,
+                       n_kv_heads=8, head_dim=128, ffn=28672, vocab=128256, rope_theta=500000.0,
+                       rope_scaling={"type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                     "high_freq_factor": 4.0,
+                                     "original_max_position_embeddings": 8192},
+                       rms_eps=1e-5, weight_qtype="Q4_K", embed_qtype="F16", output_qtype="Q4_K")
+
+
+def gpt_oss_120b_style() -> ModelConfig:
+    """gpt-oss-120B-style MoE (MXFP4 experts, bf16 attention)."""
+    return ModelConfig(name="gpt-oss-120b-style", arch="gpt-oss", n_layers=36, hidden=2880,
+                       n_heads=64, n_kv_heads=8, head_dim=64, ffn=2880, vocab=201088,
+                       rope_theta=150000.0, rope_neox=True,
+                       rope_scaling={"type": "yarn", "factor": 32.0,
+                                     "original_max_position_embeddings": 4096,
+                                     "beta_fast": 32.0, "beta_slow": 1.0},
+                       rms_eps=1e-5, attn_bias=True, attn_sinks=True, sliding_window=128,
+                       swa_every=2, n_experts=128, n_experts_used=4, expert_ffn=2880,
+                       swiglu_limit=7.0, swiglu_alpha=1.702, weight_qtype="BF16",
+                       embed_qtype="BF16", output_qtype="BF16", expert_qtype="MXFP4")
+
+
+def qwen3_next_80b_style() -> ModelConfig:
+    """Qwen3-Next-80B-A3B-style hybrid (3 DeltaNet : 1 gated attention)."""
+    return ModelConfig(name="qwen3-next-80b-a3b-style", arch="qwen3next", n_layers=48,
+                       hidden=2048, n_heads=16, n_kv_heads=2, head_dim=256, ffn=512,
+                       vocab=151936, rope_theta=10000000.0, rope_neox=True, rope_dim=64,
+                       rms_eps=1e-6, qk_norm=True, attn_output_gate=True, n_experts=512,
+                       n_experts_used=10, expert_ffn=512, shared_expert_ffn=512,
+                       moe_softmax_after_topk=False, full_attn_interval=4, ssm_k_heads=16,
+                       ssm_v_heads=32, ssm_head_dim=128, ssm_conv_kernel=4, weight_qtype="Q4_K",
+                       embed_qtype="F16", output_qtype="Q4_K", expert_qtype="Q4_K")
+
+
+PRESETS = {
+    "tiny-llama": tiny_llama,
+    "llama-3.2-3b": llama32_3b,
+    "llama-3.2-1b": llama32_1b,
+    "llama-3.3-70b": llama33_70b,
+    "gpt-oss-120b-style": gpt_oss_120b_style,
+    "qwen3-next-80b-a3b-style": qwen3_next_80b_style,
+}
+
+
+def preset(name: str) -> ModelConfig:
+    return PRESETS[name]()
+
+
+# --------------------------------------------------------------------------- GGUF mapping
+_ARCH_KEYS = {"llama": "llama", "gpt-oss": "gpt-oss", "qwen3next": "qwen3next"}
+
+
+def to_gguf_metadata(cfg: ModelConfig) -> dict:
+    a = _ARCH_KEYS[cfg.arch]
+    md = {
+        "general.name": cfg.name,
+        f"{a}.block_count": cfg.n_layers,
+        f"{a}.embedding_length": cfg.hidden,
+        f"{a}.feed_forward_length": cfg.ffn,
+        f"{a}.attention.head_count": cfg.n_heads,
+        f"{a}.attention.head_count_kv": cfg.n_kv_heads,
+        f"{a}.attention.key_length": cfg.head_dim,
+        f"{a}.attention.value_length": cfg.head_dim,
+        f"{a}.attention.layer_norm_rms_epsilon": float(cfg.rms_eps),
+        f"{a}.rope.freq_base": float(cfg.rope_theta),
+        f"{a}.rope.dimension_count": cfg.rot_dim,
+        f"{a}.vocab_size": cfg.vocab,
+    }
+    rs = cfg.rope_scaling or {}
+    if rs.get("type") in ("linear", "yarn"):
+        md[f"{a}.rope.scaling.type"] = rs["type"]
+        md[f"{a}.rope.scaling.factor"] = float(rs["factor"])
+        md[f"{a}.rope.scaling.original_context_length"] = int(
+            rs.get("original_max_position_embeddings", 4096))
+    if cfg.n_experts:
+        md[f"{a}.expert_count"] = cfg.n_experts
+        md[f"{a}.expert_used_count"] = cfg.n_experts_used
+        md[f"{a}.expert_feed_forward_length"] = cfg.expert_ffn
+        if cfg.shared_expert_ffn:
+            md[f"{a}.expert_shared_feed_forward_length"] = cfg.shared_expert_ffn
+    if cfg.sliding_window:
+        md[f"{a}.attention.sliding_window"] = cfg.sliding_window
+    if cfg.full_attn_interval:
+        md[f"{a}.full_attention_interval"] = cfg.full_attn_interval
+        md[f"{a}.ssm.conv_kernel"] = cfg.ssm_conv_kernel
+        md[f"{a}.ssm.group_count"] = cfg.ssm_k_heads
+        md[f"{a}.ssm.time_step_rank"] = cfg.ssm_v_heads
+        md[f"{a}.ssm.state_size"] = cfg.ssm_head_dim
+    # Engine-specific keys (prefixed) carry what GGUF has no standard key for.
+    md["swarmllm.config"] = __import__("json").dumps(cfg.to_dict())
+    return md
+
+
+def from_gguf_metadata(md: dict) -> ModelConfig:
+    import json
+    if "swarmllm.config" in md:
+        return ModelConfig(**json.loads(md["swarmllm.config"]))
+    arch = md["general.architecture"]
+    fam = {"llama": "llama", "gpt-oss": "gpt-oss", "qwen3next": "qwen3next"}.get(arch)
+    if fam is None:
+        raise ValueError(f"unsupported architecture {arch}")
+    a = arch
+
+    def g(k, d=None):
+        return md.get(f"{a}.{k}", d)
+
+    n_heads = g("attention.head_count")
+    hidden = g("embedding_length")
+    cfg = ModelConfig(name=md.get("general.name", arch), arch=fam, n_layers=g("block_count"),
+                      hidden=hidden, n_heads=n_heads,
+                      n_kv_heads=g("attention.head_count_kv", n_heads),
+                      head_dim=g("attention.key_length", hidden // n_heads),
+                      ffn=g("feed_forward_length", 0), vocab=g("vocab_size", 0),
+                      rope_theta=g("rope.freq_base", 10000.0),
+                      rms_eps=g("attention.layer_norm_rms_epsilon", 1e-5),
+                      rope_dim=g("rope.dimension_count", 0))
+    if g("expert_count"):
+        cfg.n_experts = g("expert_count")
+        cfg.n_experts_used = g("expert_used_count")
+        cfg.expert_ffn = g("expert_feed_forward_length", cfg.ffn)
+        cfg.shared_expert_ffn = g("expert_shared_feed_forward_length", 0)
+    if g("attention.sliding_window"):
+        cfg.sliding_window = g("attention.sliding_window")
+    if g("rope.scaling.type") in ("linear", "yarn"):
+        cfg.rope_scaling = {"type": g("rope.scaling.type"), "factor": g("rope.scaling.factor"),
+                            "original_max_position_embeddings": g("rope.scaling.original_context_length", 4096)}
+    if fam == "gpt-oss":
+        cfg.rope_neox, cfg.attn_sinks, cfg.attn_bias, cfg.swa_every = True, True, True, 2
+        cfg.swiglu_limit = 7.0
+    if fam == "qwen3next":
+        cfg.rope_neox, cfg.qk_norm, cfg.attn_output_gate = True, True, True
+        cfg.full_attn_interval = g("full_attention_interval", 4)
+        cfg.ssm_conv_kernel = g("ssm.conv_kernel", 4)
+    return cfg

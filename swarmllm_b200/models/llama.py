@@ -1,0 +1,341 @@
+"""Llama-family decoder: GPU implementation (sm_100a kernels) and a CPU
+implementation (PyTorch fp32) that doubles as the numerical oracle.
+
+Both run a *flattened mixed batch*: N token rows from any number of sequences
+(decode rows and prefill chunks together), each row with its own position,
+KV slot, block-table row and visible length.  A model instance may hold only
+a contiguous layer range (pipeline stage): the first stage embeds tokens, the
+last applies the final norm + LM head; stages exchange the fp32 residual.
+
+Per layer on the GPU (8 launches):
+  qkv GEMM -> [bias + RoPE + q/k-norm + paged KV append]      (epi_rope_kv)
+  paged attention (GQA, window, sinks)                          (decode_attn)
+  o GEMM -> [residual add + RMSNorm(ffn_norm)]                  (epi_residual_rmsnorm)
+  gate|up GEMM -> [SwiGLU]                                      (epi_swiglu)
+  down GEMM -> [residual add + RMSNorm(next attn_norm)]         (epi_residual_rmsnorm)
+Reference call stack: SplitModel::forward -> dense_layer
+(src/inference/split/executor.rs:1095,3761), LayerWeights::attend
+(src/inference/layers/mod.rs:5977).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ..gguf import quants as Q
+from ..ops.attention import AttentionWorkspace, PagedKVCache, paged_attention
+from ..ops.linear import GemmWorkspace, QLinear
+from ..utils.ext import C
+from .config import ModelConfig, rope_inv_freq
+
+
+@dataclass
+class StepBatch:
+    """Device (or CPU) tensors describing one forward's token rows."""
+    tokens: torch.Tensor        # int32 [N]
+    positions: torch.Tensor     # int32 [N]
+    slots: torch.Tensor         # int32 [N]
+    block_table: torch.Tensor   # int32 [N, max_pages]
+    seq_lens: torch.Tensor      # int32 [N] visible keys per row
+    sample_rows: torch.Tensor   # int64 [S]
+    max_len: int                # max visible length (host int, for split planning)
+    tree_mask: torch.Tensor | None = None   # uint64 [N] (as int64)
+    tree_start: torch.Tensor | None = None  # int32 [N]
+
+
+def _f32(t: torch.Tensor, qt: int, shape) -> torch.Tensor:
+    """Decode a small F32/F16 tensor given as raw bytes."""
+    arr = Q.dequantize(t.cpu().numpy().reshape(-1), qt).reshape(shape)
+    return torch.from_numpy(np.ascontiguousarray(arr, dtype=np.float32))
+
+
+class _GpuLayer:
+    pass
+
+
+class LlamaGPU:
+    def __init__(self, cfg: ModelConfig, source, device, layer_range: tuple[int, int] | None = None,
+                 kv_layer_offset: int | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        lo, hi = layer_range or (0, cfg.n_layers)
+        self.lo, self.hi = lo, hi
+        self.first, self.last = lo == 0, hi == cfg.n_layers
+        # KV caches are stage-local: layer lo of this stage is cache layer 0.
+        self.kv_off = 0 if kv_layer_offset is None else kv_layer_offset
+        dev = self.device
+        H = cfg.hidden
+
+        def get(name):
+            return source.get(name, device=dev)
+
+        def small(name):
+            t, qt, shape = source.get(name)
+            return _f32(t, qt, shape).to(dev)
+
+        if self.first:
+            t, qt, shape = get("token_embd.weight")
+            self.embd, self.embd_type = t, qt
+        self.layers = []
+        for i in range(lo, hi):
+            b = f"blk.{i}."
+            L = _GpuLayer()
+            L.attn_norm = small(b + "attn_norm.weight")
+            L.ffn_norm = small(b + "ffn_norm.weight")
+            parts = [get(b + n) for n in ("attn_q.weight", "attn_k.weight", "attn_v.weight")]
+            qt = parts[0][1]
+            assert all(p[1] == qt for p in parts), "q/k/v must share a quant type"
+            rows = sum(p[2][0] for p in parts)
+            L.wqkv = QLinear(torch.cat([p[0] for p in parts]), qt, rows, H, dev)
+            L.qkv_bias = None
+            if cfg.attn_bias:
+                L.qkv_bias = torch.cat([small(b + n) for n in
+                                        ("attn_q.bias", "attn_k.bias", "attn_v.bias")])
+            t, qt, shape = get(b + "attn_output.weight")
+            L.wo = QLinear(t, qt, shape[0], shape[1], dev)
+            L.o_bias = small(b + "attn_output.bias") if cfg.attn_bias else None
+            L.q_norm = small(b + "attn_q_norm.weight") if cfg.qk_norm else None
+            L.k_norm = small(b + "attn_k_norm.weight") if cfg.qk_norm else None
+            L.sinks = small(b + "attn_sinks.weight") if cfg.attn_sinks else None
+            L.window = cfg.sliding_window if cfg.is_swa(i) else 0
+            g, u = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
+            L.wgu = QLinear(torch.cat([g[0], u[0]]), g[1], 2 * cfg.ffn, H, dev)
+            t, qt, shape = get(b + "ffn_down.weight")
+            L.wdown = QLinear(t, qt, shape[0], shape[1], dev)
+            self.layers.append(L)
+        self.next_norm = None
+        if self.last:
+            self.out_norm = small("output_norm.weight")
+            name = "token_embd.weight" if cfg.tie_embeddings else "output.weight"
+            t, qt, shape = get(name)
+            self.head = QLinear(t, qt, shape[0], shape[1], dev)
+        inv, self.attn_factor = rope_inv_freq(cfg)
+        self.inv_freq = torch.from_numpy(inv).to(dev)
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    def weight_bytes(self) -> int:
+        n = 0
+        for L in self.layers:
+            n += L.wqkv.nbytes + L.wo.nbytes + L.wgu.nbytes + L.wdown.nbytes
+        if self.last:
+            n += self.head.nbytes
+        return n
+
+    def max_gemm_rows(self) -> int:
+        c = self.cfg
+        r = max(c.q_dim + 2 * c.kv_dim, 2 * c.ffn, c.hidden)
+        if self.last:
+            r = max(r, c.vocab)
+        return r
+
+    def make_context(self, max_tokens: int, max_samples: int, max_len: int):
+        return GpuForwardContext(self, max_tokens, max_samples, max_len)
+
+    def forward(self, b: StepBatch, kv: PagedKVCache, ctx: "GpuForwardContext",
+                h_in: torch.Tensor | None = None) -> torch.Tensor:
+        cfg = self.cfg
+        N = b.tokens.shape[0]
+        H, nq, nkv, d = cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        h = ctx.h[:N]
+        if self.first:
+            C().embed_gather(self.embd, self.embd_type, H, b.tokens, h)
+        elif h_in is not None and h_in.data_ptr() != h.data_ptr():
+            h.copy_(h_in)
+        x = ctx.x[:N]
+        C().rmsnorm(h, self.layers[0].attn_norm, x, cfg.rms_eps)
+        q = ctx.q[:N]
+        ao = ctx.attn_out[:N]
+        act = ctx.act[:N]
+        for j, L in enumerate(self.layers):
+            li = self.kv_off + j
+            g = L.wqkv(x, ctx.gemm)
+            C().epi_rope_kv(g, L.qkv_bias, b.positions, b.slots, self.inv_freq, nq, nkv, d,
+                            cfg.rot_dim, cfg.rope_neox, self.attn_factor, q, kv.k(li), kv.v(li),
+                            kv.page_size, L.q_norm, L.k_norm, cfg.rms_eps)
+            paged_attention(q, kv.k(li), kv.v(li), b.block_table, b.seq_lens, ctx.attn,
+                            ao.view(N, nq, d), b.max_len, self.scale, L.window, L.sinks,
+                            tree_mask=b.tree_mask, tree_start=b.tree_start,
+                            num_sms=ctx.gemm.num_sms)
+            g = L.wo(ao, ctx.gemm)
+            C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
+            g = L.wgu(x, ctx.gemm)
+            C().epi_swiglu(g, None, cfg.ffn, 0, False, 0.0, 0.0, act)
+            g = L.wdown(act, ctx.gemm)
+            if j + 1 < len(self.layers):
+                C().epi_residual_rmsnorm(g, h, None, self.layers[j + 1].attn_norm, x, cfg.rms_eps)
+            elif self.last:
+                C().epi_residual_rmsnorm(g, h, None, self.out_norm, x, cfg.rms_eps)
+            else:
+                C().epi_residual_rmsnorm(g, h, None, ctx.dummy_norm, None, cfg.rms_eps)
+        if not self.last:
+            return h
+        S = b.sample_rows.shape[0]
+        xs = ctx.xs[:S]
+        torch.index_select(x, 0, b.sample_rows, out=xs)
+        g = self.head(xs, ctx.gemm)
+        logits = ctx.logits[:S]
+        C().epi_copy(g, None, logits)
+        return logits
+
+
+class GpuForwardContext:
+    """Preallocated activations and scratch for one model instance."""
+
+    def __init__(self, model: LlamaGPU, max_tokens: int, max_samples: int, max_len: int):
+        cfg, dev = model.cfg, model.device
+        self.max_tokens, self.max_samples = max_tokens, max_samples
+        self.gemm = GemmWorkspace(dev, max_tokens, model.max_gemm_rows())
+        self.attn = AttentionWorkspace(dev, max_tokens, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
+                                       max_len, self.gemm.num_sms)
+        H = cfg.hidden
+        self.h = torch.zeros(max_tokens, H, dtype=torch.float32, device=dev)
+        self.x = torch.zeros(max_tokens, H, dtype=torch.float16, device=dev)
+        self.q = torch.zeros(max_tokens, cfg.n_heads, cfg.head_dim, dtype=torch.float16, device=dev)
+        self.attn_out = torch.zeros(max_tokens, cfg.q_dim, dtype=torch.float16, device=dev)
+        self.act = torch.zeros(max_tokens, cfg.ffn, dtype=torch.float16, device=dev)
+        self.xs = torch.zeros(max_samples, H, dtype=torch.float16, device=dev)
+        self.logits = torch.zeros(max_samples, cfg.vocab, dtype=torch.float32, device=dev)
+        self.dummy_norm = torch.ones(H, dtype=torch.float32, device=dev)
+        # Size the CUDA-core GEMM scratch up front (graph capture cannot grow it).
+        self.gemm.dense(max_tokens * model.max_gemm_rows() if _has_simt(model) else 0)
+
+
+def _has_simt(model: LlamaGPU) -> bool:
+    lins = []
+    for L in model.layers:
+        lins += [L.wqkv, L.wo, L.wgu, L.wdown]
+    if model.last:
+        lins.append(model.head)
+    return any(not l.use_tc for l in lins)
+
+
+# =========================================================================== CPU
+class LlamaCPU:
+    """fp32 PyTorch implementation on the host: the oracle for the GPU path and
+    the engine backend for CPU-only runs."""
+
+    def __init__(self, cfg: ModelConfig, source, layer_range: tuple[int, int] | None = None,
+                 kv_layer_offset: int | None = None, dtype=torch.float32):
+        self.cfg = cfg
+        lo, hi = layer_range or (0, cfg.n_layers)
+        self.lo, self.hi = lo, hi
+        self.first, self.last = lo == 0, hi == cfg.n_layers
+        # KV caches are stage-local: layer lo of this stage is cache layer 0.
+        self.kv_off = 0 if kv_layer_offset is None else kv_layer_offset
+        self.dtype = dtype
+
+        def dq(name):
+            t, qt, shape = source.get(name)
+            return torch.from_numpy(Q.dequantize(t.numpy().reshape(-1), qt).reshape(shape)).to(dtype)
+
+        if self.first:
+            self.embd = dq("token_embd.weight")
+        self.layers = []
+        for i in range(lo, hi):
+            b = f"blk.{i}."
+            L = _GpuLayer()
+            L.attn_norm, L.ffn_norm = dq(b + "attn_norm.weight"), dq(b + "ffn_norm.weight")
+            L.wq, L.wk, L.wv = dq(b + "attn_q.weight"), dq(b + "attn_k.weight"), dq(b + "attn_v.weight")
+            L.wo = dq(b + "attn_output.weight")
+            L.bq = dq(b + "attn_q.bias") if cfg.attn_bias else None
+            L.bk = dq(b + "attn_k.bias") if cfg.attn_bias else None
+            L.bv = dq(b + "attn_v.bias") if cfg.attn_bias else None
+            L.bo = dq(b + "attn_output.bias") if cfg.attn_bias else None
+            L.q_norm = dq(b + "attn_q_norm.weight") if cfg.qk_norm else None
+            L.k_norm = dq(b + "attn_k_norm.weight") if cfg.qk_norm else None
+            L.sinks = dq(b + "attn_sinks.weight") if cfg.attn_sinks else None
+            L.window = cfg.sliding_window if cfg.is_swa(i) else 0
+            L.wg, L.wu, L.wd = dq(b + "ffn_gate.weight"), dq(b + "ffn_up.weight"), dq(b + "ffn_down.weight")
+            self.layers.append(L)
+        if self.last:
+            self.out_norm = dq("output_norm.weight")
+            self.head = dq("token_embd.weight" if cfg.tie_embeddings else "output.weight")
+        inv, self.attn_factor = rope_inv_freq(cfg)
+        self.inv_freq = torch.from_numpy(inv)
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    def _norm(self, x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.rms_eps) * w
+
+    def _rope(self, x, pos):
+        """x [N, heads, d] -> rotated (GGML norm pairs or NEOX halves, partial)."""
+        cfg = self.cfg
+        rd = cfg.rot_dim
+        ang = pos.to(torch.float32)[:, None] * self.inv_freq[None, :]
+        c = (torch.cos(ang) * self.attn_factor)[:, None, :].to(x.dtype)
+        s = (torch.sin(ang) * self.attn_factor)[:, None, :].to(x.dtype)
+        out = x.clone()
+        if cfg.rope_neox:
+            a, b = x[..., : rd // 2], x[..., rd // 2: rd]
+            out[..., : rd // 2] = a * c - b * s
+            out[..., rd // 2: rd] = b * c + a * s
+        else:
+            a, b = x[..., 0:rd:2], x[..., 1:rd:2]
+            out[..., 0:rd:2] = a * c - b * s
+            out[..., 1:rd:2] = b * c + a * s
+        return out
+
+    def forward(self, b: StepBatch, kv: PagedKVCache, ctx=None, h_in=None) -> torch.Tensor:
+        cfg = self.cfg
+        N = b.tokens.shape[0]
+        nq, nkv, d = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        rep = nq // nkv
+        h = self.embd[b.tokens.long()].clone() if self.first else h_in.to(self.dtype).clone()
+        ps = kv.page_size
+        slots = b.slots.long()
+        pages, offs = slots // ps, slots % ps
+        for j, L in enumerate(self.layers):
+            li = self.kv_off + j
+            x = self._norm(h, L.attn_norm)
+            q = x @ L.wq.T
+            k = x @ L.wk.T
+            v = x @ L.wv.T
+            if L.bq is not None:
+                q, k, v = q + L.bq, k + L.bk, v + L.bv
+            q, k, v = q.view(N, nq, d), k.view(N, nkv, d), v.view(N, nkv, d)
+            if L.q_norm is not None:
+                q, k = self._norm(q, L.q_norm), self._norm(k, L.k_norm)
+            q, k = self._rope(q, b.positions), self._rope(k, b.positions)
+            K, V = kv.k(li), kv.v(li)
+            K[pages, :, offs, :] = k.to(K.dtype)
+            V[pages, :, offs, :] = v.to(V.dtype)
+            att = torch.empty(N, nq, d, dtype=self.dtype)
+            for t in range(N):
+                Lt = int(b.seq_lens[t])
+                lo = max(0, Lt - L.window) if L.window else 0
+                keys = torch.arange(lo, Lt)
+                bt = b.block_table[t].long()
+                kp, ko = bt[keys // ps], keys % ps
+                kk = K[kp, :, ko, :].to(self.dtype)  # [n, nkv, d]
+                vv = V[kp, :, ko, :].to(self.dtype)
+                vis = torch.ones(len(keys), dtype=torch.bool)
+                if b.tree_mask is not None:
+                    ts = int(b.tree_start[t])
+                    m = int(b.tree_mask[t]) & ((1 << 64) - 1)
+                    rel = keys - ts
+                    vis = (rel < 0) | torch.tensor([(rr >= 0 and rr < 64 and (m >> int(rr)) & 1 == 1)
+                                                    for rr in rel.tolist()], dtype=torch.bool)
+                kk = kk.repeat_interleave(rep, dim=1)
+                vv = vv.repeat_interleave(rep, dim=1)
+                s = torch.einsum("hd,nhd->hn", q[t], kk) * self.scale
+                s = s.masked_fill(~vis[None, :], float("-inf"))
+                if L.sinks is not None:
+                    s = torch.cat([s, L.sinks[:, None]], 1)
+                p = torch.softmax(s, -1)
+                if L.sinks is not None:
+                    p = p[:, :-1]
+                att[t] = torch.einsum("hn,nhd->hd", p, vv)
+            o = att.view(N, nq * d) @ L.wo.T
+            if L.bo is not None:
+                o = o + L.bo
+            h = h + o
+            x = self._norm(h, L.ffn_norm)
+            gg, uu = x @ L.wg.T, x @ L.wu.T
+            h = h + (torch.nn.functional.silu(gg) * uu) @ L.wd.T
+        if not self.last:
+            return h
+        x = self._norm(h[b.sample_rows.long()], self.out_norm)
+        return x @ self.head.T

@@ -1,0 +1,208 @@
+"""Weight sources: where a model's tensors come from.
+
+* ``GgufSource``     a GGUF file (mmap) or a shard directory (reference shard
+                     layout), tensor bytes in GGML block format.
+* ``RandomSource``   random-init weights of a given architecture, generated
+                     directly in GGML block format -- on the GPU for the big
+                     benchmark models (no 40 GB file to write), or on the host
+                     (N(0, std) floats quantized exactly) for test models.
+
+Tensor names follow the llama.cpp GGUF convention (``token_embd.weight``,
+``blk.N.attn_q.weight``, ``blk.N.ffn_down.weight``, ``output.weight`` ...).
+Every source returns ``(bytes, qtype, shape)`` with ``shape`` in numpy order.
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import torch
+
+from ..gguf import quants as Q
+from ..gguf.file import GGUFReader, GGUFWriter, ShardedGguf
+from .config import ModelConfig, from_gguf_metadata, to_gguf_metadata
+
+
+def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
+    """(name, shape, qtype) of every tensor of a model (llama.cpp names)."""
+    wq = Q.NAME_TO_TYPE[cfg.weight_qtype]
+    eq = Q.NAME_TO_TYPE[cfg.embed_qtype]
+    oq = Q.NAME_TO_TYPE[cfg.output_qtype or cfg.weight_qtype]
+    xq = Q.NAME_TO_TYPE[cfg.expert_qtype or cfg.weight_qtype]
+    H = cfg.hidden
+    specs = [("token_embd.weight", (cfg.vocab, H), eq)]
+    for i in range(cfg.n_layers):
+        b = f"blk.{i}."
+        specs.append((b + "attn_norm.weight", (H,), Q.F32))
+        if cfg.is_linear_attn(i):
+            nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
+            qkv = 2 * nk * dh + nv * dh
+            specs += [(b + "attn_qkv.weight", (qkv, H), wq),
+                      (b + "attn_gate.weight", (nv * dh, H), wq),
+                      (b + "ssm_ba.weight", (2 * nv, H), Q.F32),
+                      (b + "ssm_conv1d.weight", (qkv, cfg.ssm_conv_kernel), Q.F32),
+                      (b + "ssm_dt.bias", (nv,), Q.F32),
+                      (b + "ssm_a", (nv,), Q.F32),
+                      (b + "ssm_norm.weight", (dh,), Q.F32),
+                      (b + "ssm_out.weight", (H, nv * dh), wq)]
+        else:
+            qrows = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
+            specs += [(b + "attn_q.weight", (qrows, H), wq),
+                      (b + "attn_k.weight", (cfg.kv_dim, H), wq),
+                      (b + "attn_v.weight", (cfg.kv_dim, H), wq),
+                      (b + "attn_output.weight", (H, cfg.q_dim), wq)]
+            if cfg.attn_bias:
+                specs += [(b + "attn_q.bias", (cfg.q_dim,), Q.F32),
+                          (b + "attn_k.bias", (cfg.kv_dim,), Q.F32),
+                          (b + "attn_v.bias", (cfg.kv_dim,), Q.F32),
+                          (b + "attn_output.bias", (H,), Q.F32)]
+            if cfg.qk_norm:
+                specs += [(b + "attn_q_norm.weight", (cfg.head_dim,), Q.F32),
+                          (b + "attn_k_norm.weight", (cfg.head_dim,), Q.F32)]
+            if cfg.attn_sinks:
+                specs.append((b + "attn_sinks.weight", (cfg.n_heads,), Q.F32))
+        specs.append((b + "ffn_norm.weight", (H,), Q.F32))
+        if cfg.n_experts:
+            E, F = cfg.n_experts, cfg.expert_ffn
+            specs += [(b + "ffn_gate_inp.weight", (E, H), Q.F32),
+                      (b + "ffn_gate_exps.weight", (E, F, H), xq),
+                      (b + "ffn_up_exps.weight", (E, F, H), xq),
+                      (b + "ffn_down_exps.weight", (E, H, F), xq)]
+            if cfg.arch == "gpt-oss":
+                specs += [(b + "ffn_gate_inp.bias", (E,), Q.F32),
+                          (b + "ffn_gate_exps.bias", (E, F), Q.F32),
+                          (b + "ffn_up_exps.bias", (E, F), Q.F32),
+                          (b + "ffn_down_exps.bias", (E, H), Q.F32)]
+            if cfg.shared_expert_ffn:
+                S = cfg.shared_expert_ffn
+                specs += [(b + "ffn_gate_shexp.weight", (S, H), wq),
+                          (b + "ffn_up_shexp.weight", (S, H), wq),
+                          (b + "ffn_down_shexp.weight", (H, S), wq),
+                          (b + "ffn_gate_inp_shexp.weight", (H,), Q.F32)]
+        else:
+            specs += [(b + "ffn_gate.weight", (cfg.ffn, H), wq),
+                      (b + "ffn_up.weight", (cfg.ffn, H), wq),
+                      (b + "ffn_down.weight", (H, cfg.ffn), wq)]
+    specs.append(("output_norm.weight", (H,), Q.F32))
+    if not cfg.tie_embeddings:
+        specs.append(("output.weight", (cfg.vocab, H), oq))
+    return specs
+
+
+def _is_norm(name: str) -> bool:
+    return name.endswith("norm.weight")
+
+
+def _init_value(name: str, shape, rng: np.random.Generator, std: float) -> np.ndarray:
+    if _is_norm(name):
+        return np.ones(shape, np.float32)
+    if name.endswith("ssm_a"):
+        return -np.exp(rng.uniform(0, 1, shape)).astype(np.float32)
+    if name.endswith("ssm_dt.bias"):
+        return rng.uniform(-1, 1, shape).astype(np.float32)
+    if name.endswith("attn_sinks.weight"):
+        return rng.standard_normal(shape).astype(np.float32)
+    return (rng.standard_normal(shape, dtype=np.float32) * std).astype(np.float32)
+
+
+class GgufSource:
+    def __init__(self, path: str, layers: tuple[int, int] | None = None):
+        import os
+        if os.path.isdir(path):
+            self.f = ShardedGguf(path, layers=layers)
+        else:
+            self.f = GGUFReader(path)
+        self.cfg = from_gguf_metadata(self.f.metadata)
+
+    def has(self, name: str) -> bool:
+        return name in self.f.tensors
+
+    def get(self, name: str, device=None):
+        ti = self.f.tensors[name]
+        b = self.f.tensor_bytes(name)
+        t = torch.from_numpy(np.array(b, copy=True))
+        if device is not None:
+            t = t.to(device)
+        return t, ti.qtype, ti.shape
+
+
+class RandomSource:
+    """Deterministic random-init weights.  `device=cuda` tensors of quantized
+    types are produced directly as random GGML blocks on the GPU (values
+    roughly N(0, std)); host tensors are N(0, std) floats quantized exactly."""
+
+    def __init__(self, cfg: ModelConfig, seed: int = 0, std: float = 0.02, on_device: bool = False):
+        self.cfg, self.seed, self.std, self.on_device = cfg, seed, std, on_device
+        self.specs = {n: (s, q) for n, s, q in tensor_specs(cfg)}
+
+    def has(self, name: str) -> bool:
+        return name in self.specs
+
+    def _rng(self, name: str) -> np.random.Generator:
+        h = int.from_bytes(hashlib.sha256(f"{self.seed}:{name}".encode()).digest()[:8], "little")
+        return np.random.default_rng(h)
+
+    def get(self, name: str, device=None):
+        shape, qt = self.specs[name]
+        n = int(np.prod(shape))
+        dev_ok = device is not None and torch.device(device).type == "cuda"
+        if self.on_device and dev_ok and qt in (Q.Q4_K, Q.F16, Q.BF16, Q.MXFP4) and not _is_norm(name):
+            return _random_blocks_device(name, shape, qt, self.seed, self.std, device), qt, shape
+        vals = _init_value(name, shape, self._rng(name), self.std)
+        b = Q.quantize(vals.reshape(-1, shape[-1]), qt)
+        t = torch.from_numpy(np.ascontiguousarray(b).reshape(-1))
+        if device is not None:
+            t = t.to(device)
+        assert t.numel() == Q.nbytes(qt, n)
+        return t, qt, shape
+
+
+def _random_blocks_device(name, shape, qt, seed, std, device) -> torch.Tensor:
+    """Random GGML blocks generated on the device (uint8, flat)."""
+    h = int.from_bytes(hashlib.sha256(f"{seed}:{name}".encode()).digest()[:8], "little")
+    g = torch.Generator(device=device)
+    g.manual_seed(h & ((1 << 63) - 1))
+    n = int(np.prod(shape))
+    if qt in (Q.F16, Q.BF16):
+        dt = torch.float16 if qt == Q.F16 else torch.bfloat16
+        return (torch.randn(n, generator=g, device=device) * std).to(dt).view(torch.uint8)
+    if qt == Q.MXFP4:
+        nb = n // 32
+        out = torch.empty(nb, 17, dtype=torch.uint8, device=device)
+        # |code| up to 12 -> choose e so that 12*2^(e-128) ~ 3 std
+        e = int(round(np.log2(3 * std / 12.0))) + 128
+        out[:, 0] = e
+        out[:, 1:] = torch.randint(0, 256, (nb, 16), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+        return out.reshape(-1)
+    assert qt == Q.Q4_K
+    nb = n // 256
+    out = torch.empty(nb, 144, dtype=torch.uint8, device=device)
+    sc = torch.randint(40, 64, (nb, 8), generator=g, device=device, dtype=torch.int32)
+    m = torch.randint(40, 64, (nb, 8), generator=g, device=device, dtype=torch.int32)
+    # uniform codes 0..15 have std 4.61; per-code step s gives std ~ 4.61 s
+    s = std / 4.61
+    d = torch.full((nb,), s / 51.5, device=device, dtype=torch.float16)
+    dmin = torch.full((nb,), 7.5 * s / 51.5, device=device, dtype=torch.float16)
+    out[:, 0:2] = d.view(torch.uint8).view(nb, 2)
+    out[:, 2:4] = dmin.view(torch.uint8).view(nb, 2)
+    s12 = torch.zeros(nb, 12, dtype=torch.int32, device=device)
+    for j in range(4):
+        s12[:, j] = (sc[:, j] & 63) | ((sc[:, j + 4] >> 4) << 6)
+        s12[:, j + 4] = (m[:, j] & 63) | ((m[:, j + 4] >> 4) << 6)
+        s12[:, j + 8] = (sc[:, j + 4] & 0xF) | ((m[:, j + 4] & 0xF) << 4)
+    out[:, 4:16] = s12.to(torch.uint8)
+    out[:, 16:] = torch.randint(0, 256, (nb, 128), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+    return out.reshape(-1)
+
+
+def write_random_gguf(cfg: ModelConfig, path: str, seed: int = 0, std: float = 0.02):
+    """Write a complete random-init GGUF (host generation; for test-size models)."""
+    src = RandomSource(cfg, seed=seed, std=std)
+    w = GGUFWriter({"llama": "llama", "gpt-oss": "gpt-oss", "qwen3next": "qwen3next"}[cfg.arch])
+    for k, v in to_gguf_metadata(cfg).items():
+        w.add(k, v)
+    for name, shape, qt in tensor_specs(cfg):
+        t, _, _ = src.get(name)
+        w.add_tensor(name, t.numpy(), qt, shape)
+    w.write(path)
+    return path

@@ -1,0 +1,102 @@
+"""Quantized linear layers on the device.
+
+``QLinear`` holds one (possibly row-concatenated) GGML-quantized weight
+``[rows, K]`` and picks the kernel:
+
+* Q4_K with rows % 128 == 0 and K % 256 == 0: the tcgen05 tensor-core GEMM
+  (``qgemm_tc.cu``); the GGUF blocks are repacked on the device once at load.
+* anything else: the CUDA-core kernel over the GGUF block layout
+  (``qmatmul_simt.cu``), writing a dense fp32 result.
+
+Both return a ``GemmResult`` that the fused epilogue kernels consume.
+Row concatenation is how q|k|v and gate|up become one GEMM each: GGML rows
+are independent runs of blocks, so concatenating row bytes is exact.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from ..gguf import quants as Q
+from ..utils.ext import C
+
+
+class GemmWorkspace:
+    """Scratch shared by every GEMM of one forward: the stream-K partial
+    buffer, a dense fallback buffer and the kernel status word."""
+
+    def __init__(self, device, max_tokens: int, max_rows: int, num_sms: int | None = None):
+        self.device = torch.device(device)
+        props = torch.cuda.get_device_properties(self.device)
+        self.num_sms = num_sms or props.multi_processor_count
+        need = 0
+        for T in sorted({1, 16, 32, 64, 128, 256, max_tokens}):
+            if T > max_tokens:
+                continue
+            need = max(need, C().q4k_tc_plan(max_rows, 256 * 64, T, self.num_sms)[6])
+            need = max(need, C().q4k_tc_plan(max_rows, 256, T, self.num_sms)[6])
+        self.ws = torch.empty(int(need), dtype=torch.float32, device=self.device)
+        self._dense = torch.empty(0, dtype=torch.float32, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.max_tokens = max_tokens
+        self.max_rows = max_rows
+
+    def dense(self, n: int) -> torch.Tensor:
+        """fp32 scratch of at least n floats for the CUDA-core GEMM (grows
+        outside CUDA-graph capture only)."""
+        if self._dense.numel() < n:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("GEMM scratch must be sized before CUDA-graph capture")
+            self._dense = torch.empty(n, dtype=torch.float32, device=self.device)
+        return self._dense
+
+    def check(self):
+        """Raise if a kernel wait timed out (status word set on the device)."""
+        s = int(self.status.item())
+        if s:
+            raise RuntimeError(f"GPU kernel reported a timed-out wait (code {s})")
+
+
+class QLinear:
+    def __init__(self, data, qtype: int, rows: int, K: int, device, bias: np.ndarray | None = None,
+                 force_simt: bool = False):
+        self.qtype, self.rows, self.K = qtype, rows, K
+        self.device = torch.device(device)
+        raw = data if isinstance(data, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(data))
+        raw = raw.reshape(-1).to(self.device, dtype=torch.uint8)
+        self.use_tc = (qtype == Q.Q4_K and rows % 128 == 0 and K % 256 == 0 and not force_simt)
+        if self.use_tc:
+            self.packed = torch.empty(rows * (K // 256) * 144, dtype=torch.uint8, device=self.device)
+            C().q4k_repack(raw, rows, K, self.packed)
+            self.raw = None
+        else:
+            self.raw = raw
+            self.packed = None
+        self.bias = None
+        if bias is not None:
+            self.bias = torch.as_tensor(bias, dtype=torch.float32, device=self.device)
+
+    @property
+    def nbytes(self) -> int:
+        t = self.packed if self.use_tc else self.raw
+        return t.numel()
+
+    def __call__(self, x: torch.Tensor, ws: GemmWorkspace):
+        T = x.shape[0]
+        if self.use_tc:
+            return C().qgemm_q4k_tc(self.packed, self.rows, self.K, x, ws.ws, ws.status, ws.num_sms)
+        out = ws.dense(T * self.rows)[: T * self.rows].view(T, self.rows)
+        return C().qmatmul_simt(self.raw, self.qtype, self.rows, self.K, x, out)
+
+    def reference(self, x: torch.Tensor, ws: GemmWorkspace):
+        """Same product through the CUDA-core kernel (on-device oracle)."""
+        raw = self.raw
+        if raw is None:
+            raise ValueError("reference() needs the GGUF-layout bytes (construct with force_simt)")
+        out = torch.empty(x.shape[0], self.rows, dtype=torch.float32, device=self.device)
+        return C().qmatmul_simt(raw, self.qtype, self.rows, self.K, x, out)
+
+
+def concat_rows(parts: list[np.ndarray]) -> np.ndarray:
+    """Concatenate quantized row blocks [rows_i, row_bytes] along rows."""
+    return np.concatenate([np.asarray(p, dtype=np.uint8).reshape(p.shape[0], -1) for p in parts], 0)

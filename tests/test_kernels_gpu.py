@@ -1,0 +1,279 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from swarmllm_b200.gguf import quants as Q
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def C():
+    from swarmllm_b200.utils.ext import C as _C
+    return _C()
+
+
+def rel_err(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / (b.norm() + 1e-30))
+
+
+def _x(T, K, seed=0, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(T, K, generator=g) * scale).to(torch.float16)
+
+
+@pytest.mark.parametrize("qt", [Q.Q4_0, Q.Q8_0, Q.Q4_K, Q.Q6_K, Q.IQ4_NL, Q.IQ4_XS, Q.MXFP4,
+                                Q.F16, Q.BF16, Q.F32])
+@pytest.mark.parametrize("T", [1, 5, 11])
+def test_qmatmul_simt(qt, T):
+    rows, K = 96, 512
+    rng = np.random.default_rng(1)
+    w = rng.standard_normal((rows, K), dtype=np.float32) * 0.02
+    b = Q.quantize(w, qt)
+    wd = torch.from_numpy(Q.dequantize(b, qt))
+    x = _x(T, K)
+    ref = x.float() @ wd.T
+    out = torch.empty(T, rows, dtype=torch.float32, device=DEV)
+    C().qmatmul_simt(torch.from_numpy(b).to(DEV), qt, rows, K, x.to(DEV), out)
+    assert rel_err(out.cpu(), ref) < 1e-4
+
+
+def _dense_from(g, T, rows):
+    out = torch.empty(T, rows, dtype=torch.float32, device=DEV)
+    C().epi_copy(g, None, out)
+    return out
+
+
+@pytest.mark.parametrize("rows,K", [(128, 256), (384, 1024), (1024, 4096), (256, 8192)])
+@pytest.mark.parametrize("T", [1, 7, 16, 33, 64, 130, 256, 300])
+def test_qgemm_q4k_tc(rows, K, T):
+    rng = np.random.default_rng(rows + K)
+    w = rng.standard_normal((rows, K), dtype=np.float32) * 0.02
+    b = Q.quantize(w, Q.Q4_K)
+    wd = torch.from_numpy(Q.dequantize(b, Q.Q4_K))
+    x = _x(T, K, seed=T)
+    ref = x.float() @ wd.T
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    ws = GemmWorkspace(DEV, max(T, 1), rows)
+    lin = QLinear(b, Q.Q4_K, rows, K, DEV)
+    assert lin.use_tc
+    g = lin(x.to(DEV), ws)
+    out = _dense_from(g, T, rows)
+    torch.cuda.synchronize()
+    ws.check()
+    e = rel_err(out.cpu(), ref)
+    assert e < 3e-3, e
+
+
+def test_q4k_repack_matches_host():
+    rows, K = 256, 512
+    rng = np.random.default_rng(3)
+    b = Q.quantize(rng.standard_normal((rows, K), dtype=np.float32) * 0.02, Q.Q4_K)
+    dst = torch.empty(rows * (K // 256) * 144, dtype=torch.uint8, device=DEV)
+    C().q4k_repack(torch.from_numpy(b).to(DEV), rows, K, dst)
+    host = Q.q4k_repack_host(b, rows, K).reshape(-1)
+    assert np.array_equal(dst.cpu().numpy(), host)
+
+
+def test_qgemm_tc_stream_k_many_segments():
+    """K long enough that tiles split across several CTAs."""
+    rows, K, T = 128, 256 * 96, 3
+    rng = np.random.default_rng(5)
+    b = Q.quantize(rng.standard_normal((rows, K), dtype=np.float32) * 0.02, Q.Q4_K)
+    wd = torch.from_numpy(Q.dequantize(b, Q.Q4_K))
+    x = _x(T, K, seed=9)
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    ws = GemmWorkspace(DEV, T, rows)
+    g = QLinear(b, Q.Q4_K, rows, K, DEV)(x.to(DEV), ws)
+    assert g.upc < g.ksb  # really split
+    out = _dense_from(g, T, rows)
+    assert rel_err(out.cpu(), x.float() @ wd.T) < 3e-3
+
+
+# ----------------------------------------------------------------------------- epilogues
+def _gemm_identity(vals):
+    """GemmResult whose content equals `vals` [T, R] (F32 identity weight)."""
+    T, R = vals.shape
+    w = torch.eye(R, dtype=torch.float32)
+    x = vals.to(torch.float16)
+    out = torch.empty(T, R, dtype=torch.float32, device=DEV)
+    g = C().qmatmul_simt(w.view(torch.uint8).reshape(-1).to(DEV), Q.F32, R, R, x.to(DEV), out)
+    return g, x.float()
+
+
+def test_epi_residual_rmsnorm():
+    T, H = 5, 256
+    g, v = _gemm_identity(torch.randn(T, H))
+    res = torch.randn(T, H)
+    w = torch.rand(H) + 0.5
+    rd = res.clone().to(DEV)
+    out = torch.empty(T, H, dtype=torch.float16, device=DEV)
+    C().epi_residual_rmsnorm(g, rd, None, w.to(DEV), out, 1e-5)
+    h = res + v
+    ref = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5) * w
+    assert rel_err(rd.cpu(), h) < 1e-6
+    assert rel_err(out.float().cpu(), ref) < 2e-3
+
+
+@pytest.mark.parametrize("neox,rope_dim", [(False, 64), (True, 64), (True, 32)])
+def test_epi_rope_kv(neox, rope_dim):
+    T, nq, nkv, d, ps = 6, 4, 2, 64, 16
+    R = (nq + 2 * nkv) * d
+    g, v = _gemm_identity(torch.randn(T, R))
+    pos = torch.tensor([0, 3, 17, 100, 4095, 9], dtype=torch.int32)
+    slots = torch.tensor([5, 16, 33, 2, 40, 63], dtype=torch.int32)
+    inv = 1.0 / (10000 ** (torch.arange(0, rope_dim, 2, dtype=torch.float64) / rope_dim))
+    inv = inv.float()
+    q = torch.empty(T, nq, d, dtype=torch.float16, device=DEV)
+    kc = torch.zeros(4, nkv, ps, d, dtype=torch.float16, device=DEV)
+    vc = torch.zeros_like(kc)
+    C().epi_rope_kv(g, None, pos.to(DEV), slots.to(DEV), inv.to(DEV), nq, nkv, d, rope_dim, neox,
+                    1.0, q, kc, vc, ps, None, None, 1e-6)
+    x = v.view(T, nq + 2 * nkv, d)
+
+    def rope(t):
+        ang = pos.double()[:, None] * inv.double()[None]
+        c, s = torch.cos(ang)[:, None], torch.sin(ang)[:, None]
+        o = t.double().clone()
+        if neox:
+            a, b = t[..., :rope_dim // 2].double(), t[..., rope_dim // 2:rope_dim].double()
+            o[..., :rope_dim // 2] = a * c - b * s
+            o[..., rope_dim // 2:rope_dim] = b * c + a * s
+        else:
+            a, b = t[..., 0:rope_dim:2].double(), t[..., 1:rope_dim:2].double()
+            o[..., 0:rope_dim:2] = a * c - b * s
+            o[..., 1:rope_dim:2] = b * c + a * s
+        return o
+    qr = rope(x[:, :nq])
+    kr = rope(x[:, nq:nq + nkv])
+    assert rel_err(q.double().cpu(), qr) < 2e-3
+    kc, vc = kc.cpu(), vc.cpu()
+    for t in range(T):
+        p, o = int(slots[t]) // ps, int(slots[t]) % ps
+        assert rel_err(kc[p, :, o].double(), kr[t]) < 2e-3
+        assert rel_err(vc[p, :, o].double(), x[t, nq + nkv:].double()) < 2e-3
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+def test_epi_swiglu(kind):
+    T, F = 3, 256
+    g, v = _gemm_identity(torch.randn(T, 2 * F) * 3)
+    out = torch.empty(T, F, dtype=torch.float16, device=DEV)
+    C().epi_swiglu(g, None, F, kind, False, 1.702, 7.0, out)
+    gg, uu = v[:, :F], v[:, F:]
+    if kind == 0:
+        ref = torch.nn.functional.silu(gg) * uu
+    else:
+        x = gg.clamp(max=7.0)
+        u = uu.clamp(-7.0, 7.0)
+        ref = x * torch.sigmoid(1.702 * x) * (u + 1)
+    assert rel_err(out.float().cpu(), ref) < 2e-3
+
+
+# ----------------------------------------------------------------------------- attention
+def _attn_ref(q, K, V, bt, lens, ps, scale, window=0, sinks=None, tmask=None, tstart=None):
+    T, nq, d = q.shape
+    nkv = K.shape[1]
+    rep = nq // nkv
+    out = torch.zeros(T, nq, d, dtype=torch.float64)
+    for t in range(T):
+        L = int(lens[t])
+        lo = max(0, L - window) if window else 0
+        keys = torch.arange(lo, L)
+        pg = bt[t].long()[keys // ps]
+        kk = K[pg, :, keys % ps].double().repeat_interleave(rep, 1)
+        vv = V[pg, :, keys % ps].double().repeat_interleave(rep, 1)
+        s = torch.einsum("hd,nhd->hn", q[t].double(), kk) * scale
+        if tmask is not None:
+            vis = torch.tensor([(k < int(tstart[t])) or (k - int(tstart[t]) < 64 and
+                               (int(tmask[t]) >> (k - int(tstart[t]))) & 1 == 1) for k in keys.tolist()])
+            s = s.masked_fill(~vis[None], float("-inf"))
+        if sinks is not None:
+            s = torch.cat([s, sinks.double()[:, None]], 1)
+        p = torch.softmax(s, -1)
+        if sinks is not None:
+            p = p[:, :-1]
+        out[t] = torch.einsum("hn,nhd->hd", p, vv)
+    return out
+
+
+@pytest.mark.parametrize("d,nq,nkv", [(128, 64, 8), (128, 24, 8), (64, 64, 8), (256, 16, 2)])
+@pytest.mark.parametrize("window,sinks", [(0, False), (128, True)])
+def test_paged_decode_attention(d, nq, nkv, window, sinks):
+    from swarmllm_b200.ops.attention import AttentionWorkspace, paged_attention
+    torch.manual_seed(0)
+    ps, P = 16, 64
+    lens = torch.tensor([1, 17, 300, 700], dtype=torch.int32)
+    T = lens.numel()
+    K = torch.randn(P, nkv, ps, d).half()
+    V = torch.randn(P, nkv, ps, d).half()
+    bt = torch.stack([torch.randperm(P)[:48] for _ in range(T)]).int()
+    q = torch.randn(T, nq, d).half()
+    sk = torch.randn(nq) if sinks else None
+    scale = 1 / math.sqrt(d)
+    ws = AttentionWorkspace(DEV, T, nq, nkv, d, 768)
+    out = torch.empty(T, nq, d, dtype=torch.float16, device=DEV)
+    paged_attention(q.to(DEV), K.to(DEV), V.to(DEV), bt.to(DEV), lens.to(DEV), ws, out, 768, scale,
+                    window, sk.to(DEV) if sinks else None)
+    ref = _attn_ref(q, K, V, bt, lens, ps, scale, window, sk)
+    assert rel_err(out.double().cpu(), ref) < 3e-3
+
+
+def test_paged_attention_tree_mask():
+    from swarmllm_b200.ops.attention import AttentionWorkspace, paged_attention
+    torch.manual_seed(1)
+    d, nq, nkv, ps, P = 128, 16, 4, 16, 16
+    T = 5
+    base = 40
+    lens = torch.full((T,), base + 5, dtype=torch.int32)
+    tmask = torch.tensor([0b1, 0b11, 0b101, 0b1011, 0b10101], dtype=torch.int64)
+    tstart = torch.full((T,), base, dtype=torch.int32)
+    K = torch.randn(P, nkv, ps, d).half()
+    V = torch.randn(P, nkv, ps, d).half()
+    bt = torch.arange(P).int()[None].repeat(T, 1)
+    q = torch.randn(T, nq, d).half()
+    ws = AttentionWorkspace(DEV, T, nq, nkv, d, 64)
+    out = torch.empty(T, nq, d, dtype=torch.float16, device=DEV)
+    paged_attention(q.to(DEV), K.to(DEV), V.to(DEV), bt.to(DEV), lens.to(DEV), ws, out, 64,
+                    1 / math.sqrt(d), tree_mask=tmask.to(DEV), tree_start=tstart.to(DEV))
+    ref = _attn_ref(q, K, V, bt, lens, ps, 1 / math.sqrt(d), tmask=tmask, tstart=tstart)
+    assert rel_err(out.double().cpu(), ref) < 3e-3
+
+
+# ----------------------------------------------------------------------------- sampling
+def test_argmax_and_sampling():
+    from swarmllm_b200.engine.sampling import SamplingParams, sample_host
+    torch.manual_seed(0)
+    V = 50000
+    logits = torch.randn(6, V) * 3
+    out = torch.empty(6, dtype=torch.int32, device=DEV)
+    C().argmax(logits.to(DEV), out, None)
+    assert torch.equal(out.cpu().long(), logits.argmax(-1))
+    params = [SamplingParams(temperature=0.8, seed=11), SamplingParams(temperature=1.0, top_k=20, seed=3),
+              SamplingParams(temperature=0.7, top_p=0.9, seed=5), SamplingParams(temperature=0.0),
+              SamplingParams(temperature=1.3, top_k=5, top_p=0.8, seed=99),
+              SamplingParams(temperature=0.5, seed=123456789012)]
+    pos = np.array([0, 5, 9, 3, 1000, 77], dtype=np.int32)
+    dev_out = torch.empty(6, dtype=torch.int32, device=DEV)
+    C().sample(logits.to(DEV), torch.tensor([p.temperature for p in params]).to(DEV),
+               torch.tensor([p.top_k for p in params], dtype=torch.int32).to(DEV),
+               torch.tensor([p.top_p for p in params]).to(DEV),
+               torch.tensor([p.seed for p in params], dtype=torch.int64).to(DEV),
+               torch.from_numpy(pos).to(DEV), dev_out)
+    host = sample_host(logits, params, pos)
+    assert dev_out.cpu().numpy().tolist() == host.tolist()
+
+
+def test_philox_matches_host():
+    from swarmllm_b200.engine.sampling import philox_uniform_host
+    pos = torch.tensor([0, 7, 123456], dtype=torch.int32)
+    out = torch.empty(3, 1000, dtype=torch.float32, device=DEV)
+    C().philox_uniform(987654321, pos.to(DEV), 1000, out)
+    for r in range(3):
+        h = philox_uniform_host(987654321, int(pos[r]), np.arange(1000))
+        assert np.array_equal(out[r].cpu().numpy(), h)

@@ -1,0 +1,85 @@
+"""GPU model vs the CPU fp32 oracle, and the GPU engine end to end."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def _cfg(qt="Q4_K", layers=2):
+    from swarmllm_b200.models.config import ModelConfig
+    return ModelConfig(name="t", arch="llama", n_layers=layers, hidden=512, n_heads=8, n_kv_heads=2,
+                       head_dim=64, ffn=1024, vocab=1024, weight_qtype=qt, embed_qtype="F16",
+                       output_qtype=qt, rope_scaling={"type": "llama3", "factor": 8.0,
+                                                      "original_max_position_embeddings": 64})
+
+
+def _batch(tokens, positions, slots, bt, device, sample_rows):
+    from swarmllm_b200.models.llama import StepBatch
+    t = lambda a, dt=torch.int32: torch.as_tensor(np.asarray(a), dtype=dt, device=device)
+    return StepBatch(t(tokens), t(positions), t(slots), t(bt), t(np.asarray(positions) + 1),
+                     t(sample_rows, torch.int64), 256)
+
+
+@pytest.mark.parametrize("qt", ["Q4_K", "Q8_0", "Q6_K"])
+def test_gpu_forward_matches_cpu_oracle(qt):
+    from swarmllm_b200.models.llama import LlamaCPU, LlamaGPU
+    from swarmllm_b200.models.weights import RandomSource
+    from swarmllm_b200.ops.attention import PagedKVCache
+    cfg = _cfg(qt)
+    src = RandomSource(cfg, seed=3)
+    gpu = LlamaGPU(cfg, src, DEV)
+    cpu = LlamaCPU(cfg, src)
+    ctx = gpu.make_context(64, 8, 256)
+    kvg = PagedKVCache(cfg.n_layers, 8, cfg.n_kv_heads, cfg.head_dim, DEV)
+    kvc = PagedKVCache(cfg.n_layers, 8, cfg.n_kv_heads, cfg.head_dim, "cpu", dtype=torch.float32)
+    rng = np.random.default_rng(0)
+    # prefill 40 tokens of one sequence, then 3 decode steps
+    toks = rng.integers(0, cfg.vocab, 43)
+    bt = np.tile(np.arange(8, dtype=np.int32), (64, 1))
+    pos = np.arange(40)
+    lg = gpu.forward(_batch(toks[:40], pos, pos, bt[:40], DEV, [39]), kvg, ctx)
+    lc = cpu.forward(_batch(toks[:40], pos, pos, bt[:40], "cpu", [39]), kvc)
+    cos = torch.nn.functional.cosine_similarity(lg.cpu().double(), lc.double(), dim=-1)
+    assert float(cos.min()) > 0.999, cos
+    for p in range(40, 43):
+        lg = gpu.forward(_batch([toks[p]], [p], [p], bt[:1], DEV, [0]), kvg, ctx)
+        lc = cpu.forward(_batch([toks[p]], [p], [p], bt[:1], "cpu", [0]), kvc)
+        cos = torch.nn.functional.cosine_similarity(lg.cpu().double(), lc.double(), dim=-1)
+        assert float(cos.min()) > 0.999, (p, cos)
+
+
+def test_engine_graphs_match_eager():
+    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = _cfg()
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, cfg.vocab, n).tolist() for n in (5, 37, 64, 100)]
+    res = []
+    for graphs in (False, True):
+        eng = LLMEngine.from_config(cfg, DEV, EngineConfig(max_model_len=256, max_running=8,
+                                                           max_step_tokens=128, prefill_chunk=64,
+                                                           cuda_graphs=graphs, graph_sizes=(1, 2, 4, 8)),
+                                    source=RandomSource(cfg, seed=5))
+        outs = eng.generate(prompts, SamplingParams(max_tokens=12))
+        res.append([o.token_ids for o in outs])
+    assert res[0] == res[1]
+
+
+def test_engine_gpu_vs_cpu_greedy_tokens():
+    """Greedy continuation: GPU and CPU engines agree on (almost) every token."""
+    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = _cfg("Q8_0")
+    rng = np.random.default_rng(2)
+    prompts = [rng.integers(0, cfg.vocab, 24).tolist() for _ in range(3)]
+    ec = EngineConfig(max_model_len=128, max_running=4, max_step_tokens=128, prefill_chunk=128,
+                      graph_sizes=(1, 2, 4))
+    g = LLMEngine.from_config(cfg, DEV, ec, source=RandomSource(cfg, seed=7)).generate(
+        prompts, SamplingParams(max_tokens=8))
+    c = LLMEngine.from_config(cfg, "cpu", ec, source=RandomSource(cfg, seed=7)).generate(
+        prompts, SamplingParams(max_tokens=8))
+    agree = np.mean([a == b for og, oc in zip(g, c) for a, b in zip(og.token_ids, oc.token_ids)])
+    assert agree >= 0.9, (agree, [o.token_ids for o in g], [o.token_ids for o in c])
