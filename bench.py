@@ -106,6 +106,10 @@ def reference_arm(args):
                       "registry exists offline"}))
 
 
+def log(msg):
+    print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def single_gpu(args):
     import numpy as np
     import torch
@@ -124,6 +128,8 @@ def single_gpu(args):
     t0 = time.time()
     eng = LLMEngine.from_config(cfg, dev, ecfg, seed=1234)
     t_init = time.time() - t0
+    log(f"engine ready in {t_init:.1f}s; weights {eng.model.weight_bytes() / 1e9:.1f} GB, "
+        f"kv pages {eng.bm.num_pages}")
     rng = np.random.default_rng(0)
     sp = SamplingParams(max_tokens=G, ignore_eos=True)
 
@@ -141,12 +147,15 @@ def single_gpu(args):
         ttfts.append((time.perf_counter() - t) * 1e3)
         eng.release(rid)
     ttft_p50 = statistics.median(ttfts[1:])  # first run includes one-time setup
+    log(f"ttft runs (ms): {[round(t, 1) for t in ttfts]}")
 
     def decode_rate(batch: int, steps: int, warmup: int):
         rids = [eng.add_request(rng.integers(0, cfg.vocab, P).tolist(), sp) for _ in range(batch)]
         # run until every sequence is decoding
+        t_pf = time.time()
         while eng.sched.num_waiting or any(len(eng.output(r)) == 0 for r in rids):
             eng.step()
+        log(f"batch {batch}: prefill of {batch}x{P} tokens took {time.time() - t_pf:.1f}s")
         for _ in range(warmup):
             eng.step()
         runner = eng.runner

@@ -18,6 +18,16 @@ from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 import pybind11
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+
+# Use the system toolchain (dynamic libstdc++ shared with torch).  A compiler
+# that links libstdc++ statically gives the extension private iostream/locale
+# state, and formatting a number into a torch error message then crashes.
+if not os.environ.get("SWARMLLM_KEEP_CXX"):
+    for _var, _exe in (("CC", "/usr/bin/gcc"), ("CXX", "/usr/bin/g++")):
+        if os.path.exists(_exe):
+            os.environ[_var] = _exe
+    if os.path.exists("/usr/bin/g++"):
+        os.environ["LDSHARED"] = "/usr/bin/g++ -shared"
 CSRC = os.path.join("swarmllm_b200", "csrc")
 
 NVCC_FLAGS = [

@@ -4,6 +4,11 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <execinfo.h>
+#include <signal.h>
+#include <unistd.h>
+
+#include <cstdlib>
 
 #include "kernels.h"
 #include "gemm_out.cuh"
@@ -134,6 +139,7 @@ GemmResult qgemm_q4k_tc(Tensor w_packed, int64_t rows, int64_t K, Tensor x, Tens
                         Tensor status, int64_t num_sms) {
   CHECK_CUDA(w_packed); CHECK_CUDA(x); CHECK_DT(x, at::kHalf); CHECK_DT(ws, at::kFloat);
   CHECK_DT(status, at::kInt);
+  TORCH_CHECK(status.numel() >= 8, "status must hold 8 ints");
   TORCH_CHECK(x.size(-1) == K && x.stride(-1) == 1, "x must be [T, K] with unit inner stride");
   const at::cuda::CUDAGuard guard(x.device());
   const int T = (int)x.size(0);
@@ -208,8 +214,23 @@ void philox_uniform(int64_t seed, Tensor positions, int64_t V, Tensor out) {
                         (int)V, out.data_ptr<float>(), cur_stream());
 }
 
+// SWARMLLM_SEGV_BT=1: print a native backtrace on SIGSEGV (debug aid for
+// host-side crashes; there is no debugger on the GPU boxes).
+static void segv_handler(int sig) {
+  void* frames[64];
+  int n = backtrace(frames, 64);
+  const char msg[] = "\n[swarmllm] native backtrace:\n";
+  (void)!write(2, msg, sizeof(msg) - 1);
+  backtrace_symbols_fd(frames, n, 2);
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "swarmllm_b200 sm_100a kernels";
+  if (const char* e = getenv("SWARMLLM_SEGV_BT")) {
+    if (e[0] == '1') signal(SIGSEGV, segv_handler);
+  }
   py::class_<GemmResult>(m, "GemmResult")
       .def_property_readonly("rows", [](const GemmResult& r) { return r.g.rows; })
       .def_property_readonly("T", [](const GemmResult& r) { return r.g.T; })

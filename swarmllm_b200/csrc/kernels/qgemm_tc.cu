@@ -28,8 +28,8 @@
 //    sum the slots while reading (gemm_out.cuh).
 //
 // Warp roles: warp 0 = bulk/TMA producer, warp 1 = TMEM owner + MMA issuer,
-// warps 2.. = 2 dequantizer warpgroups (alternate units), which also drain
-// the accumulator for the segments they finish.
+// warps 2.. = 2 dequantizer warpgroups (alternate units); warpgroup 0 also
+// drains the accumulator at the end of every tile segment.
 #include "kernels.h"
 #include "gemm_out.cuh"
 #include "tc_utils.cuh"
@@ -114,7 +114,7 @@ SW_DEVICE bool dq_half(const uint4 (&q)[8], const float* sc, const float* mb, in
                        uint32_t tmem_lane_base, uint64_t* a_empty, uint64_t* a_full, int lane,
                        int* status) {
   const int j = 2 * unit + H, as = j % kAStages;
-  if (!mbar_wait(&a_empty[as], ((j / kAStages) & 1) ^ 1, status, 32)) return false;
+  if (!mbar_wait_warp(&a_empty[as], ((j / kAStages) & 1) ^ 1, status, 32, unit, j)) return false;
   tc_fence_after();
   const uint32_t taddr = tmem_lane_base + kAColBase + as * 64;
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
@@ -190,14 +190,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int tile = (int)(u / a.ksb), sb = (int)(u - (long)tile * a.ksb);
         const int rt = tile / a.n_tok_tiles, nt = tile - rt * a.n_tok_tiles;
         const int wsi = i % C::W_ST;
-        if (!(ok = mbar_wait(&w_empty[wsi], ((i / C::W_ST) & 1) ^ 1, a.status, 11))) break;
+        if (!(ok = mbar_wait(&w_empty[wsi], ((i / C::W_ST) & 1) ^ 1, a.status, 11, i, 0))) break;
         mbar_arrive_expect_tx(&w_full[wsi], kWStageBytes);
         bulk_load(w_smem + wsi * kWStageBytes,
                   a.w + ((size_t)rt * a.ksb + sb) * kWStageBytes, kWStageBytes, &w_full[wsi]);
         ++issued_w;
         for (int h = 0; h < 2; ++h) {
           const int j = 2 * i + h, xs = j % C::X_ST;
-          if (!(ok = mbar_wait(&x_empty[xs], ((j / C::X_ST) & 1) ^ 1, a.status, 12))) break;
+          if (!(ok = mbar_wait(&x_empty[xs], ((j / C::X_ST) & 1) ^ 1, a.status, 12, i, j))) break;
           mbar_arrive_expect_tx(&x_full[xs], C::X_HALF_BYTES);
           uint8_t* dst = x_smem + xs * C::X_HALF_BYTES;
           const int k0 = sb * 256 + h * 128;
@@ -226,13 +226,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool first = (i == 0) || (sb == 0);
         const bool last = (i == n_units - 1) || (sb == a.ksb - 1);
         if (first && seg > 0) {
-          if (!(ok = mbar_wait(d_empty, (seg - 1) & 1, a.status, 21))) break;
+          if (!(ok = mbar_wait(d_empty, (seg - 1) & 1, a.status, 21, i, seg))) break;
           tc_fence_after();
         }
         for (int h = 0; h < 2; ++h) {
           const int j = 2 * i + h, as = j % kAStages, xs = j % C::X_ST;
-          if (!(ok = mbar_wait(&a_full[as], (j / kAStages) & 1, a.status, 22))) break;
-          if (!(ok = mbar_wait(&x_full[xs], (j / C::X_ST) & 1, a.status, 23))) break;
+          if (!(ok = mbar_wait(&a_full[as], (j / kAStages) & 1, a.status, 22, i, j))) break;
+          if (!(ok = mbar_wait(&x_full[xs], (j / C::X_ST) & 1, a.status, 23, i, j))) break;
           tc_fence_after();
           const uint32_t xb = smem_u32(x_smem + xs * C::X_HALF_BYTES);
 #pragma unroll
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool last = (i == n_units - 1) || (sb == a.ksb - 1);
       if ((i % kDqWG) == g) {
         const int wsi = i % C::W_ST;
-        if (!(ok = mbar_wait(&w_full[wsi], (i / C::W_ST) & 1, a.status, 31))) break;
+        if (!(ok = mbar_wait_warp(&w_full[wsi], (i / C::W_ST) & 1, a.status, 31, i, 0))) break;
         const uint4* src = reinterpret_cast<const uint4*>(w_smem + wsi * kWStageBytes +
                                                            row * kQ4kRowBytes);
         uint4 q[8];
@@ -285,9 +285,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!ok) break;
       }
       if (last) {
-        if ((i % kDqWG) == g) {
+        // Warpgroup 0 drains every segment.  Alternating drainers would let a
+        // warpgroup wait on d_full two phases ahead after a one-unit segment,
+        // where a parity wait passes too early.
+        if (g == 0) {
           // Drain the accumulator of this tile segment into workspace slot (tile + cta).
-          if (!(ok = mbar_wait(d_full, seg & 1, a.status, 33))) break;
+          if (!(ok = mbar_wait_warp(d_full, seg & 1, a.status, 33, i, seg))) break;
           tc_fence_after();
           const int nt = tile % a.n_tok_tiles;
           const int n_valid = min(N, a.T - nt * N);
@@ -312,6 +315,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }

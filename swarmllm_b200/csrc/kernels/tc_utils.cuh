@@ -57,7 +57,10 @@ SW_DEVICE bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 
 // Wait until the phase with `parity` has completed.  Bounded: on timeout the
 // status word gets `code` and the function returns false.
-SW_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+// status (if given) is an int[8]: [0] first failing code, [1] block, [2..3]
+// caller details, [4] parity, [5] thread.
+SW_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, int d0 = 0,
+                         int d1 = 0) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = globaltimer();
@@ -65,10 +68,28 @@ SW_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) 
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(addr, parity)) return true;
     if (globaltimer() - t0 > kWaitTimeoutNs) {
-      if (status) atomicCAS(status, 0, code);
+      if (status && atomicCAS(status, 0, code) == 0) {
+        status[1] = blockIdx.x;
+        status[2] = d0;
+        status[3] = d1;
+        status[4] = (int)parity;
+        status[5] = threadIdx.x;
+      }
       return false;
     }
   }
+}
+
+// Warp-uniform wait: lane 0 spins, the result is broadcast and the warp is
+// reconverged, so `.sync.aligned` tcgen05 instructions that follow are executed
+// by all 32 lanes together.  Call from all lanes of the warp.
+SW_DEVICE bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int* status, int code, int d0 = 0,
+                              int d1 = 0) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, code, d0, d1) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
 }
 
 // 2D tiled TMA load (no multicast) completing on `bar`.

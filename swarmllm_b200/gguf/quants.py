@@ -224,7 +224,7 @@ def dequantize(data: np.ndarray, qtype: int, n_values: int | None = None) -> np.
     blocks = data.reshape(-1, bb)
     out = {Q4_0: _dq4_0, Q8_0: _dq8_0, Q4_K: _dq4_k, Q6_K: _dq6_k, IQ4_NL: _diq4_nl,
            IQ4_XS: _diq4_xs, MXFP4: _dmxfp4}[qtype](blocks)
-    return out.reshape(lead + (-1,))
+    return out.astype(np.float32, copy=False).reshape(lead + (-1,))
 
 
 def _dq8_0(b):

@@ -29,15 +29,17 @@ class GemmWorkspace:
         self.device = torch.device(device)
         props = torch.cuda.get_device_properties(self.device)
         self.num_sms = num_sms or props.multi_processor_count
+        # Stream-K slots: (tiles + CTAs) x tok_tile x 128 floats, CTAs <= num_sms.
         need = 0
         for T in sorted({1, 16, 32, 64, 128, 256, max_tokens}):
             if T > max_tokens:
                 continue
-            need = max(need, C().q4k_tc_plan(max_rows, 256 * 64, T, self.num_sms)[6])
-            need = max(need, C().q4k_tc_plan(max_rows, 256, T, self.num_sms)[6])
+            n_tok = C().q4k_tc_plan(128, 256, T, self.num_sms)[0]
+            tiles = (max_rows + 127) // 128 * ((T + n_tok - 1) // n_tok)
+            need = max(need, (tiles + self.num_sms) * n_tok * 128)
         self.ws = torch.empty(int(need), dtype=torch.float32, device=self.device)
         self._dense = torch.empty(0, dtype=torch.float32, device=self.device)
-        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(8, dtype=torch.int32, device=self.device)
         self.max_tokens = max_tokens
         self.max_rows = max_rows
 
@@ -52,9 +54,10 @@ class GemmWorkspace:
 
     def check(self):
         """Raise if a kernel wait timed out (status word set on the device)."""
-        s = int(self.status.item())
-        if s:
-            raise RuntimeError(f"GPU kernel reported a timed-out wait (code {s})")
+        s = self.status.cpu().tolist()
+        if s[0]:
+            raise RuntimeError(f"GPU kernel reported a timed-out wait: code {s[0]} block {s[1]} "
+                               f"detail {s[2]},{s[3]} parity {s[4]} thread {s[5]}")
 
 
 class QLinear:

@@ -80,6 +80,28 @@ def test_q4k_repack_matches_host():
     assert np.array_equal(dst.cpu().numpy(), host)
 
 
+@pytest.mark.parametrize("rows,K,T,sms", [(1280, 2048, 1, 9), (1280, 2048, 33, 9),
+                                          (1024, 2048, 1, 2), (1024, 2048, 17, 2), (1024, 2048, 1, 3),
+                                          (1024, 2048, 40, 3), (1024, 2048, 130, 1),
+                                          (128, 2048, 1, 1), (256, 2048, 5, 3), (384, 3072, 40, 7),
+                                          (1024, 4096, 16, 5), (512, 1024, 300, 4),
+                                          (256, 28672, 32, 148), (8192 // 8, 8192, 2, 148)])
+def test_qgemm_tc_multi_unit_ctas(rows, K, T, sms):
+    """Few CTAs: each processes many units and crosses tile boundaries."""
+    rng = np.random.default_rng(rows * 7 + T)
+    b = Q.quantize(rng.standard_normal((rows, K), dtype=np.float32) * 0.02, Q.Q4_K)
+    wd = torch.from_numpy(Q.dequantize(b, Q.Q4_K))
+    x = _x(T, K, seed=T + 1)
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    ws = GemmWorkspace(DEV, T, rows, num_sms=sms)
+    lin = QLinear(b, Q.Q4_K, rows, K, DEV)
+    g = lin(x.to(DEV), ws)
+    out = _dense_from(g, T, rows)
+    torch.cuda.synchronize()
+    ws.check()
+    assert rel_err(out.cpu(), x.float() @ wd.T) < 3e-3
+
+
 def test_qgemm_tc_stream_k_many_segments():
     """K long enough that tiles split across several CTAs."""
     rows, K, T = 128, 256 * 96, 3
