@@ -154,6 +154,11 @@ GemmResult qgemm_q4k_tc(Tensor w_packed, int64_t rows, int64_t K, Tensor x, Tens
   return r;
 }
 
+void qgemm_set_trace_py(OptT buf) {
+  if (buf.has_value()) TORCH_CHECK(buf->numel() * buf->element_size() >= 512 * 8 * 8, "trace buffer too small");
+  qgemm_set_trace(ptr_or_null<void>(buf));
+}
+
 void q4k_repack(Tensor src, int64_t rows, int64_t K, Tensor dst) {
   CHECK_CUDA(src); CHECK_CUDA(dst);
   TORCH_CHECK(K % 256 == 0, "K must be a multiple of 256");
@@ -249,6 +254,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("q4k_tc_plan", &q4k_tc_plan_py);
   m.def("qgemm_q4k_tc", &qgemm_q4k_tc);
   m.def("q4k_repack", &q4k_repack);
+  m.def("qgemm_set_trace", &qgemm_set_trace_py);
   m.def("decode_attn", &decode_attn);
   m.def("argmax", &argmax);
   m.def("sample", &sample);

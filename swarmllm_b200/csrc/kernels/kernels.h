@@ -41,6 +41,7 @@ void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_
 int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, int x_stride,
                         int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
                         swarm::GemmOut* out, cudaStream_t s);
+void qgemm_set_trace(void* buf);
 int launch_q4k_repack(const void* src, int rows, int K, void* dst, cudaStream_t s);
 int make_tmap_2d_16bit(CUtensorMap* map, const void* base, int rows, int cols, int row_stride,
                        int box_rows, int box_cols, int swizzle_bytes);

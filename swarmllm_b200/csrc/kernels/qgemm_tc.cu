@@ -28,8 +28,9 @@
 //    sum the slots while reading (gemm_out.cuh).
 //
 // Warp roles: warp 0 = bulk/TMA producer, warp 1 = TMEM owner + MMA issuer,
-// warps 2.. = 2 dequantizer warpgroups (alternate units); warpgroup 0 also
-// drains the accumulator at the end of every tile segment.
+// warps 2.. = 3 (token tile <= 128) or 2 dequantizer warpgroups taking units
+// round-robin; warpgroup 0 also drains the accumulator at the end of every
+// tile segment.
 #include "kernels.h"
 #include "gemm_out.cuh"
 #include "tc_utils.cuh"
@@ -40,20 +41,31 @@ using namespace tc;
 constexpr int kQ4kRowBytes = 144;
 constexpr int kWStageBytes = 128 * kQ4kRowBytes;  // 18432
 constexpr int kTmemCols = 512;
-constexpr int kAColBase = 256;
-constexpr int kAStages = 4;  // 64 TMEM columns each = 128 K fp16 values
-constexpr int kDqWG = 2;     // dequantizer warpgroups
-constexpr int kGemmThreads = 64 + 128 * kDqWG;
 
+// Per token-tile configuration.  Each dequantizer warpgroup owns its own pair
+// of TMEM A stages and its own W stages (the stage counts are multiples of the
+// warpgroup count), so a stage is always re-used by the warpgroup that used it
+// last and no parity wait can run two phases ahead.
 template <int N>
 struct QCfg {
-  static constexpr int X_HALF_BYTES = N * 256;
-  static constexpr int X_ST = N <= 64 ? 8 : (N <= 128 ? 4 : 2);
-  static constexpr int W_ST = 4;
-  static constexpr int X_BYTES = X_ST * X_HALF_BYTES;
+  // Dequantizer warpgroups take units round-robin; each owns one "unit stage":
+  // 128 TMEM columns of A (K=256 fp16) plus the unit's activation tile in smem,
+  // released by one MMA commit.  Stage counts are multiples of DQ, so every
+  // stage is re-used by the warpgroup that used it last and no parity wait can
+  // run two phases ahead.
+  static constexpr int DQ = N <= 64 ? 3 : 2;
+  static constexpr int U = DQ;                           // unit stages in flight
+  static constexpr int THREADS = 96 + 128 * DQ;          // W producer, MMA, X producer, DQ WGs
+  static constexpr int FIRST_DQ_WARP = 3;
+  static constexpr int A_COL = kTmemCols - 128 * U;      // D uses columns [0, N)
+  static constexpr int X_UNIT_BYTES = N * 512;           // N rows x 256 K fp16 (4 swizzle atoms)
+  static constexpr int W_ST = 2 * DQ;
+  static_assert(A_COL >= N, "TMEM budget");
+  static constexpr int X_BYTES = U * X_UNIT_BYTES;
   static constexpr int W_BYTES = W_ST * kWStageBytes;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SMEM = 1024 + X_BYTES + W_BYTES + BAR_BYTES;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
 struct QGemmArgs {
@@ -64,7 +76,15 @@ struct QGemmArgs {
   int upc;
   float* ws;
   int* status;
+  unsigned long long* trace;  // debug: per-unit event timestamps of CTA 0 (null = off)
 };
+
+// Debug timeline of CTA 0 (see qgemm_set_trace): trace[unit*8 + event] = %globaltimer.
+#define QTRACE(tr, unit, ev)                                                           \
+  do {                                                                                 \
+    if ((tr) != nullptr && blockIdx.x == 0 && (unit) < 512) (tr)[(unit) * 8 + (ev)] = \
+        globaltimer();                                                                 \
+  } while (0)
 
 SW_DEVICE __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 SW_DEVICE uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -107,36 +127,22 @@ SW_DEVICE void q4k_decode_scales(const uint4& hdr, float* s, float* mb) {
 #undef SB
 }
 
-// Dequantize half H (K 128*H .. 128*H+127) of one row's superblock into TMEM
-// A stage (2*unit + H) % kAStages.
-template <int H>
-SW_DEVICE bool dq_half(const uint4 (&q)[8], const float* sc, const float* mb, int unit,
-                       uint32_t tmem_lane_base, uint64_t* a_empty, uint64_t* a_full, int lane,
-                       int* status) {
-  const int j = 2 * unit + H, as = j % kAStages;
-  if (!mbar_wait_warp(&a_empty[as], ((j / kAStages) & 1) ^ 1, status, 32, unit, j)) return false;
-  tc_fence_after();
-  const uint32_t taddr = tmem_lane_base + kAColBase + as * 64;
+// Dequantize one row's superblock (256 K values) into the unit's 128 TMEM columns.
+SW_DEVICE void dq_unit(const uint4 (&q)[8], const float* sc, const float* mb, uint32_t taddr) {
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
 #pragma unroll
-  for (int sbk = 0; sbk < 4; ++sbk) {
-    const int sub = 4 * H + sbk;
+  for (int sub = 0; sub < 8; ++sub) {
     const __half2 S = __float2half2_rn(sc[sub]), S16 = __float2half2_rn(sc[sub] * 0.0625f);
     const __half2 MB = __float2half2_rn(-mb[sub]);
     uint32_t cols[16];
 #pragma unroll
-    for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[16 * H + 4 * sbk + w4], S, S16, MB, cols + 4 * w4);
-    tmem_st_x16(taddr + sbk * 16, cols);
+    for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[4 * sub + w4], S, S16, MB, cols + 4 * w4);
+    tmem_st_x16(taddr + sub * 16, cols);
   }
-  tmem_wait_st();
-  tc_fence_before();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(&a_full[as]);
-  return true;
 }
 
 template <int N>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
     qgemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap x_map, QGemmArgs a) {
   using C = QCfg<N>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -145,13 +151,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* x_smem = smem;
   uint8_t* w_smem = smem + C::X_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_smem + C::W_BYTES);
-  uint64_t* w_full = bars;
-  uint64_t* w_empty = w_full + C::W_ST;
-  uint64_t* x_full = w_empty + C::W_ST;
-  uint64_t* x_empty = x_full + C::X_ST;
-  uint64_t* a_full = x_empty + C::X_ST;
-  uint64_t* a_empty = a_full + kAStages;
-  uint64_t* d_full = a_empty + kAStages;
+  uint64_t* w_full = bars;                 // W stage loaded (tx)
+  uint64_t* w_empty = w_full + C::W_ST;    // W stage read by its warpgroup (4 warps)
+  uint64_t* ready = w_empty + C::W_ST;     // unit: A in TMEM (4 warps) + X in smem (producer + tx)
+  uint64_t* empty = ready + C::U;          // unit consumed by the MMAs (commit)
+  uint64_t* d_full = empty + C::U;
   uint64_t* d_empty = d_full + 1;
   uint64_t* done_bar = d_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
@@ -163,8 +167,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::W_ST; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
-    for (int i = 0; i < C::X_ST; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
-    for (int i = 0; i < kAStages; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < C::U; ++i) { mbar_init(&ready[i], 5); mbar_init(&empty[i], 1); }
     mbar_init(d_full, 1);
     mbar_init(d_empty, 4);
     mbar_init(done_bar, 1);
@@ -181,75 +184,82 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ W producer
     if (lane == 0) {
-      int issued_w = 0, issued_x = 0;
+      int issued = 0;
       bool ok = true;
-      for (int i = 0; i < n_units && ok; ++i) {
-        const long u = u0 + i;
-        const int tile = (int)(u / a.ksb), sb = (int)(u - (long)tile * a.ksb);
-        const int rt = tile / a.n_tok_tiles, nt = tile - rt * a.n_tok_tiles;
+      int tile = (int)(u0 / a.ksb), sb = (int)(u0 - (long)tile * a.ksb);
+      for (int i = 0; i < n_units && ok; ++i, (++sb == a.ksb) ? (sb = 0, ++tile) : 0) {
+        const int rt = tile / a.n_tok_tiles;
         const int wsi = i % C::W_ST;
         if (!(ok = mbar_wait(&w_empty[wsi], ((i / C::W_ST) & 1) ^ 1, a.status, 11, i, 0))) break;
+        QTRACE(a.trace, i, 0);
         mbar_arrive_expect_tx(&w_full[wsi], kWStageBytes);
         bulk_load(w_smem + wsi * kWStageBytes,
                   a.w + ((size_t)rt * a.ksb + sb) * kWStageBytes, kWStageBytes, &w_full[wsi]);
-        ++issued_w;
-        for (int h = 0; h < 2; ++h) {
-          const int j = 2 * i + h, xs = j % C::X_ST;
-          if (!(ok = mbar_wait(&x_empty[xs], ((j / C::X_ST) & 1) ^ 1, a.status, 12, i, j))) break;
-          mbar_arrive_expect_tx(&x_full[xs], C::X_HALF_BYTES);
-          uint8_t* dst = x_smem + xs * C::X_HALF_BYTES;
-          const int k0 = sb * 256 + h * 128;
-          tma_load_2d(dst, &x_map, k0, nt * N, &x_full[xs]);
-          tma_load_2d(dst + N * 128, &x_map, k0 + 64, nt * N, &x_full[xs]);
-          ++issued_x;
-        }
+        ++issued;
       }
-      if (!ok) {
-        // Drain our own copies still in flight before the CTA exits.
-        for (int i = max(0, issued_w - C::W_ST); i < issued_w; ++i)
+      if (!ok)  // drain our own copies still in flight before the CTA exits
+        for (int i = max(0, issued - C::W_ST); i < issued; ++i)
           mbar_wait(&w_full[i % C::W_ST], (i / C::W_ST) & 1, nullptr, 0);
-        for (int j = max(0, issued_x - C::X_ST); j < issued_x; ++j)
-          mbar_wait(&x_full[j % C::X_ST], (j / C::X_ST) & 1, nullptr, 0);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ X producer
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      int tile = (int)(u0 / a.ksb), sb = (int)(u0 - (long)tile * a.ksb);
+      for (int i = 0; i < n_units && ok; ++i, (++sb == a.ksb) ? (sb = 0, ++tile) : 0) {
+        const int nt = tile % a.n_tok_tiles;
+        const int s = i % C::U;
+        if (!(ok = mbar_wait(&empty[s], ((i / C::U) & 1) ^ 1, a.status, 12, i, 0))) break;
+        mbar_arrive_expect_tx(&ready[s], C::X_UNIT_BYTES);
+        uint8_t* dst = x_smem + s * C::X_UNIT_BYTES;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tma_load_2d(dst + c * (N * 128), &x_map, sb * 256 + c * 64, nt * N, &ready[s]);
+        QTRACE(a.trace, i, 1);
+        ++issued;
       }
+      if (!ok)
+        for (int i = max(0, issued - C::U); i < issued; ++i)
+          mbar_wait(&ready[i % C::U], (i / C::U) & 1, nullptr, 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(128, N, /*f16*/ 0);
+      // Descriptor of each X stage; per-MMA K offsets are compile-time adds to
+      // the start-address field (16-byte units).
+      uint64_t xdesc[C::U];
+#pragma unroll
+      for (int st = 0; st < C::U; ++st)
+        xdesc[st] = smem_desc(smem_u32(x_smem + st * C::X_UNIT_BYTES), 16, 1024, 2);
       int seg = 0;
       bool ok = true;
-      for (int i = 0; i < n_units && ok; ++i) {
-        const long u = u0 + i;
-        const int sb = (int)(u % a.ksb);
+      int sb = (int)(u0 % a.ksb);
+      for (int i = 0; i < n_units && ok; ++i, (++sb == a.ksb) ? (sb = 0) : 0) {
         const bool first = (i == 0) || (sb == 0);
         const bool last = (i == n_units - 1) || (sb == a.ksb - 1);
         if (first && seg > 0) {
           if (!(ok = mbar_wait(d_empty, (seg - 1) & 1, a.status, 21, i, seg))) break;
-          tc_fence_after();
         }
-        for (int h = 0; h < 2; ++h) {
-          const int j = 2 * i + h, as = j % kAStages, xs = j % C::X_ST;
-          if (!(ok = mbar_wait(&a_full[as], (j / kAStages) & 1, a.status, 22, i, j))) break;
-          if (!(ok = mbar_wait(&x_full[xs], (j / C::X_ST) & 1, a.status, 23, i, j))) break;
-          tc_fence_after();
-          const uint32_t xb = smem_u32(x_smem + xs * C::X_HALF_BYTES);
+        const int s = i % C::U;
+        if (!(ok = mbar_wait(&ready[s], (i / C::U) & 1, a.status, 22, i, 0))) break;
+        QTRACE(a.trace, i, 5);
+        tc_fence_after();
+        const uint64_t xd = xdesc[0] + (uint64_t)((s * C::X_UNIT_BYTES) >> 4);
+        const uint32_t ab = tmem_base + C::A_COL + s * 128;
+        umma_f16_ts(tmem_base, ab, xd, idesc, first ? 0u : 1u);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t a_t = tmem_base + kAColBase + as * 64 + kk * 8;
-            const uint64_t bd =
-                smem_desc(xb + (kk >> 2) * (N * 128) + (kk & 3) * 32, 16, 1024, /*sw128*/ 2);
-            umma_f16_ts(tmem_base, a_t, bd, idesc, (first && h == 0 && kk == 0) ? 0u : 1u);
-          }
-          umma_commit(&a_empty[as]);
-          umma_commit(&x_empty[xs]);
-        }
-        if (!ok) break;
+        for (int kk = 1; kk < 16; ++kk)
+          umma_f16_ts(tmem_base, ab + kk * 8, xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4),
+                      idesc, 1u);
+        umma_commit(&empty[s]);
         if (last) {
           umma_commit(d_full);
           ++seg;
         }
+        QTRACE(a.trace, i, 6);
       }
       // All MMAs issued by this thread have completed once done_bar flips.
       umma_commit(done_bar);
@@ -257,19 +267,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ dequant + epilogue
-    const int g = (warp - 2) >> 2;      // warpgroup
-    const int quad = warp & 3;          // TMEM lane quadrant this warp may touch
-    const int row = quad * 32 + lane;   // weight row inside the 128-row tile
+    const int g = (warp - C::FIRST_DQ_WARP) >> 2;  // warpgroup
+    const int quad = warp & 3;                       // TMEM lane quadrant this warp may touch
+    const int row = quad * 32 + lane;                // weight row inside the 128-row tile
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    unsigned long long* tr = ((warp - C::FIRST_DQ_WARP) % 4 == 0) ? a.trace : nullptr;
     int seg = 0;
     bool ok = true;
-    for (int i = 0; i < n_units && ok; ++i) {
-      const long u = u0 + i;
-      const int tile = (int)(u / a.ksb), sb = (int)(u - (long)tile * a.ksb);
+    int tile = (int)(u0 / a.ksb), sb = (int)(u0 - (long)tile * a.ksb);
+    for (int i = 0; i < n_units && ok; ++i, (++sb == a.ksb) ? (sb = 0, ++tile) : 0) {
       const bool last = (i == n_units - 1) || (sb == a.ksb - 1);
-      if ((i % kDqWG) == g) {
+      if ((i % C::DQ) == g) {
         const int wsi = i % C::W_ST;
         if (!(ok = mbar_wait_warp(&w_full[wsi], (i / C::W_ST) & 1, a.status, 31, i, 0))) break;
+        if (lane == 0) QTRACE(tr, i, 2);
         const uint4* src = reinterpret_cast<const uint4*>(w_smem + wsi * kWStageBytes +
                                                            row * kQ4kRowBytes);
         uint4 q[8];
@@ -280,16 +291,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) mbar_arrive(&w_empty[wsi]);
         float sc_f[8], mb_f[8];
         q4k_decode_scales(hdr, sc_f, mb_f);
-        ok = dq_half<0>(q, sc_f, mb_f, i, tmem_base + lane_off, a_empty, a_full, lane, a.status) &&
-             dq_half<1>(q, sc_f, mb_f, i, tmem_base + lane_off, a_empty, a_full, lane, a.status);
-        if (!ok) break;
+        const int s = i % C::U;
+        if (!(ok = mbar_wait_warp(&empty[s], ((i / C::U) & 1) ^ 1, a.status, 32, i, 0))) break;
+        if (lane == 0) QTRACE(tr, i, 7);
+        tc_fence_after();
+        dq_unit(q, sc_f, mb_f, tmem_base + lane_off + C::A_COL + s * 128);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[s]);
+        if (lane == 0) QTRACE(tr, i, 3);
       }
       if (last) {
         // Warpgroup 0 drains every segment.  Alternating drainers would let a
         // warpgroup wait on d_full two phases ahead after a one-unit segment,
         // where a parity wait passes too early.
         if (g == 0) {
-          // Drain the accumulator of this tile segment into workspace slot (tile + cta).
           if (!(ok = mbar_wait_warp(d_full, seg & 1, a.status, 33, i, seg))) break;
           tc_fence_after();
           const int nt = tile % a.n_tok_tiles;
@@ -393,12 +410,17 @@ int make_tmap_2d_16bit(CUtensorMap* map, const void* base, int rows, int cols, i
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+static unsigned long long* g_trace = nullptr;
+
+// Debug: record the event timeline of CTA 0 of every following launch into
+// `buf` (device, >= 512*8 u64); nullptr turns it off.
+void qgemm_set_trace(void* buf) { g_trace = static_cast<unsigned long long*>(buf); }
+
 int q4k_tc_tok_tile(int T) {
   if (T <= 16) return 16;
   if (T <= 32) return 32;
   if (T <= 64) return 64;
-  if (T <= 128) return 128;
-  return 256;
+  return 128;  // N=128 already runs the tensor core at full rate (48..69 clk per K=16 MMA)
 }
 
 // Work decomposition shared by the launcher, the workspace sizing and GemmOut.
@@ -430,7 +452,7 @@ static int launch_n(const CUtensorMap& map, const QGemmArgs& a, int n_ctas, cuda
       return -3;
     attr_set = true;
   }
-  qgemm_q4k_tc_kernel<N><<<n_ctas, kGemmThreads, C::SMEM, s>>>(map, a);
+  qgemm_q4k_tc_kernel<N><<<n_ctas, C::THREADS, C::SMEM, s>>>(map, a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -447,14 +469,13 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
   if (need > ws_floats_avail) return -6;
   CUtensorMap map;
   if (make_tmap_2d_16bit(&map, x, T, K, x_stride, N, 64, 128) != 0) return -2;
-  QGemmArgs a{(const uint8_t*)w_packed, rows, K, T, ntt, kb, total, upc, ws, status};
+  QGemmArgs a{(const uint8_t*)w_packed, rows, K, T, ntt, kb, total, upc, ws, status, g_trace};
   int rc;
   switch (N) {
     case 16: rc = launch_n<16>(map, a, ctas, s); break;
     case 32: rc = launch_n<32>(map, a, ctas, s); break;
     case 64: rc = launch_n<64>(map, a, ctas, s); break;
-    case 128: rc = launch_n<128>(map, a, ctas, s); break;
-    default: rc = launch_n<256>(map, a, ctas, s); break;
+    default: rc = launch_n<128>(map, a, ctas, s); break;
   }
   if (out) {
     out->ws = ws;

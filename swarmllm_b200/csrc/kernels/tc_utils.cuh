@@ -55,6 +55,21 @@ SW_DEVICE bool mbar_try_wait(uint32_t addr, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps (up to `ns`) until the
+// phase completes instead of re-polling, so waiting warps do not take issue
+// slots from the warps doing the work.
+SW_DEVICE bool mbar_try_wait_sleep(uint32_t addr, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with `parity` has completed.  Bounded: on timeout the
 // status word gets `code` and the function returns false.
 // status (if given) is an int[8]: [0] first failing code, [1] block, [2..3]
@@ -65,8 +80,8 @@ SW_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, 
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(addr, parity)) return true;
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait_sleep(addr, parity, 20000u)) return true;
     if (globaltimer() - t0 > kWaitTimeoutNs) {
       if (status && atomicCAS(status, 0, code) == 0) {
         status[1] = blockIdx.x;
