@@ -194,6 +194,37 @@ void decode_attn(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, T
   TORCH_CHECK(rc == 0, "decode_attn: unsupported head_dim/group size");
 }
 
+void attn_tc(Tensor q, Tensor k_cache, Tensor v_cache, Tensor group_row0, Tensor group_npos,
+             int64_t pos_per_group, Tensor block_table, Tensor seq_lens, OptT tree_mask,
+             OptT tree_start, OptT sinks, int64_t window, double scale, int64_t keys_per_split,
+             int64_t n_splits, Tensor out, Tensor part_o, Tensor part_ml, Tensor status) {
+  CHECK_DT(q, at::kHalf); CHECK_DT(k_cache, at::kHalf); CHECK_DT(v_cache, at::kHalf);
+  CHECK_DT(block_table, at::kInt); CHECK_DT(seq_lens, at::kInt); CHECK_DT(out, at::kHalf);
+  CHECK_DT(group_row0, at::kInt); CHECK_DT(group_npos, at::kInt); CHECK_DT(status, at::kInt);
+  CHECK_CONTIG(q); CHECK_CONTIG(out); CHECK_CONTIG(block_table); CHECK_CONTIG(k_cache);
+  TORCH_CHECK(status.numel() >= 8, "status must hold 8 ints");
+  const at::cuda::CUDAGuard guard(q.device());
+  const int T = (int)q.size(0), n_q = (int)q.size(1), d = (int)q.size(2);
+  const int n_kv = (int)k_cache.size(1);
+  TORCH_CHECK(k_cache.size(2) == 16 && k_cache.size(3) == d, "cache must be [pages, n_kv, 16, d]");
+  const int G = (int)group_row0.numel();
+  int rc = launch_attn_tc(
+      reinterpret_cast<const __half*>(q.data_ptr()), T, n_q,
+      reinterpret_cast<const __half*>(k_cache.data_ptr()),
+      reinterpret_cast<const __half*>(v_cache.data_ptr()), (long)k_cache.size(0), n_kv, d,
+      group_row0.data_ptr<int32_t>(), group_npos.data_ptr<int32_t>(), G, (int)pos_per_group,
+      block_table.data_ptr<int32_t>(), (int)block_table.stride(0), seq_lens.data_ptr<int32_t>(),
+      ptr_or_null<uint64_t>(tree_mask), ptr_or_null<int32_t>(tree_start), ptr_or_null<float>(sinks),
+      (int)window, (float)scale, (int)keys_per_split, (int)n_splits,
+      reinterpret_cast<__half*>(out.data_ptr()), part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+      status.data_ptr<int>(), cur_stream());
+  TORCH_CHECK(rc == 0, "attn_tc launch failed: rc=", rc);
+  if (n_splits > 1)
+    launch_attn_combine(part_o.data_ptr<float>(), part_ml.data_ptr<float>(), T * n_q, (int)n_splits,
+                        d, ptr_or_null<float>(sinks), n_q, reinterpret_cast<__half*>(out.data_ptr()),
+                        cur_stream());
+}
+
 // ---------------------------------------------------------------- sampling
 void argmax(Tensor logits, Tensor out, OptT out_val) {
   CHECK_DT(logits, at::kFloat); CHECK_DT(out, at::kInt);
@@ -256,6 +287,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("q4k_repack", &q4k_repack);
   m.def("qgemm_set_trace", &qgemm_set_trace_py);
   m.def("decode_attn", &decode_attn);
+  m.def("attn_tc", &attn_tc);
+  m.def("attn_set_trace", [](OptT buf) { attn_set_trace(ptr_or_null<void>(buf)); });
   m.def("argmax", &argmax);
   m.def("sample", &sample);
   m.def("philox_uniform", &philox_uniform);

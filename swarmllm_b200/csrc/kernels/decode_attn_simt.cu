@@ -214,3 +214,11 @@ int launch_decode_attn_simt(const __half* q, const __half* k_cache, const __half
   SW_LAUNCH_CHECK();
   return 0;
 }
+
+// Merge split-KV partials of any attention kernel (SIMT or tcgen05).
+void launch_attn_combine(const float* part_o, const float* part_ml, int rows, int n_splits, int D,
+                         const float* sinks, int n_q, __half* out, cudaStream_t s) {
+  if (rows <= 0) return;
+  decode_attn_combine_kernel<<<rows, 128, 0, s>>>(part_o, part_ml, n_splits, D, sinks, n_q, out);
+  SW_LAUNCH_CHECK();
+}

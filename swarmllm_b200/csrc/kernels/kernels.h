@@ -55,6 +55,17 @@ int launch_decode_attn_simt(const __half* q, const __half* k_cache, const __half
                             int keys_per_split, int n_splits, float* part_o, float* part_ml,
                             __half* out, cudaStream_t s);
 
+void attn_set_trace(void* buf);
+void launch_attn_combine(const float* part_o, const float* part_ml, int rows, int n_splits, int D,
+                         const float* sinks, int n_q, __half* out, cudaStream_t s);
+int launch_attn_tc(const __half* q, int T, int n_q, const __half* k_cache, const __half* v_cache,
+                   long num_pages, int n_kv, int D, const int32_t* group_row0,
+                   const int32_t* group_npos, int G, int pos_per_group, const int32_t* block_table,
+                   int bt_stride, const int32_t* seq_lens, const uint64_t* tree_mask,
+                   const int32_t* tree_start, const float* sinks, int window, float scale,
+                   int keys_per_split, int n_splits, __half* out, float* part_o, float* part_ml,
+                   int* status, cudaStream_t s);
+
 // ---- sampling -----------------------------------------------------------------
 void launch_argmax(const float* logits, int rows, int V, int stride, int32_t* out, float* out_val,
                    cudaStream_t s);

@@ -79,9 +79,12 @@ SW_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code, 
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = globaltimer();
+  // Plain try_wait polling: its built-in suspend wakes on phase completion.
+  // (A suspend-time hint compiles to timed sleeps that add microseconds of
+  // latency to every hand-off.)
   while (true) {
-    for (int i = 0; i < 8; ++i)
-      if (mbar_try_wait_sleep(addr, parity, 20000u)) return true;
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(addr, parity)) return true;
     if (globaltimer() - t0 > kWaitTimeoutNs) {
       if (status && atomicCAS(status, 0, code) == 0) {
         status[1] = blockIdx.x;
@@ -113,6 +116,15 @@ SW_DEVICE void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 3D tiled TMA load (no multicast) completing on `bar`.
+SW_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 

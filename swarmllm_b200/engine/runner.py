@@ -39,6 +39,22 @@ def plan_arrays(plan, block_manager, max_pages: int):
     return tokens, positions, slots, bt_rows, seq_lens, sample_rows
 
 
+def attention_groups(plan, n_rep: int):
+    """Row groups for the tensor-core attention kernel: runs of at most
+    128 // n_rep consecutive positions of one sequence (None if every
+    sequence contributes a single row, i.e. pure decode)."""
+    ntok = plan.seq_ntok
+    if len(ntok) == 0 or int(np.max(ntok)) <= 1:
+        return None
+    ppg = max(1, 128 // n_rep)
+    r0, npos = [], []
+    for st, n in zip(plan.seq_start, ntok):
+        for o in range(0, int(n), ppg):
+            r0.append(int(st) + o)
+            npos.append(min(ppg, int(n) - o))
+    return np.asarray(r0, np.int32), np.asarray(npos, np.int32), ppg
+
+
 class GpuRunner:
     def __init__(self, model, kv: PagedKVCache, max_tokens: int, max_seqs: int, max_model_len: int,
                  graph_sizes=(1, 2, 4, 8, 16, 32, 64), use_graphs: bool = True, trash_page: int = -1):
@@ -150,7 +166,13 @@ class GpuRunner:
             res = out[:S]
         else:
             M, _ = self._upload(tokens, positions, slots, bt_rows, seq_lens, sample_rows)
-            logits = self.model.forward(self._batch(M, S), self.kv, self.ctx)
+            b = self._batch(M, S)
+            cfg = self.model.cfg
+            grp = attention_groups(plan, cfg.n_heads // cfg.n_kv_heads)
+            if grp is not None:
+                b.groups = (torch.from_numpy(grp[0]).to(self.device, non_blocking=True),
+                            torch.from_numpy(grp[1]).to(self.device, non_blocking=True), grp[2])
+            logits = self.model.forward(b, self.kv, self.ctx)
             res = self.sampler.sample(logits, params, positions[sample_rows] if S else [])
         self.h_out[:S].copy_(res, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()

@@ -44,6 +44,7 @@ class StepBatch:
     max_len: int                # max visible length (host int, for split planning)
     tree_mask: torch.Tensor | None = None   # uint64 [N] (as int64)
     tree_start: torch.Tensor | None = None  # int32 [N]
+    groups: tuple | None = None             # (row0 int32[G], npos int32[G], positions/group)
 
 
 def _f32(t: torch.Tensor, qt: int, shape) -> torch.Tensor:
@@ -158,7 +159,7 @@ class LlamaGPU:
             paged_attention(q, kv.k(li), kv.v(li), b.block_table, b.seq_lens, ctx.attn,
                             ao.view(N, nq, d), b.max_len, self.scale, L.window, L.sinks,
                             tree_mask=b.tree_mask, tree_start=b.tree_start,
-                            num_sms=ctx.gemm.num_sms)
+                            num_sms=ctx.gemm.num_sms, groups=b.groups)
             g = L.wo(ao, ctx.gemm)
             C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
             g = L.wgu(x, ctx.gemm)

@@ -41,8 +41,19 @@ class PagedKVCache:
         d[:, :, dp, :, do, :] = rows
 
 
+def tc_split_plan(n_groups: int, n_kv: int, max_len: int, num_sms: int = 148,
+                  max_splits: int = 32) -> tuple[int, int]:
+    """(keys_per_split, n_splits) for the tcgen05 kernel: whole 128-key tiles,
+    enough CTAs for about two waves."""
+    tiles = max(1, (max_len + 127) // 128)
+    ctas = max(1, n_groups * n_kv)
+    want = max(1, min(tiles, max_splits, (2 * num_sms + ctas - 1) // ctas))
+    tps = (tiles + want - 1) // want
+    return tps * 128, (tiles + tps - 1) // tps
+
+
 class AttentionWorkspace:
-    """Split-KV partial buffers for the decode attention kernel."""
+    """Split-KV partial buffers and status word for the attention kernels."""
 
     def __init__(self, device, max_rows: int, n_q: int, n_kv: int, head_dim: int, max_len: int,
                  num_sms: int = 148, max_splits: int = 32):
@@ -51,7 +62,8 @@ class AttentionWorkspace:
         t = 1
         while True:
             tt = min(t, max_rows)
-            worst = max(worst, tt * split_plan(tt, n_kv, max_len, num_sms, max_splits)[1])
+            worst = max(worst, tt * split_plan(tt, n_kv, max_len, num_sms, max_splits)[1],
+                        tt * tc_split_plan(tt, n_kv, max_len, num_sms, max_splits)[1])
             if tt == max_rows:
                 break
             t *= 2
@@ -59,6 +71,11 @@ class AttentionWorkspace:
         self.part_o = torch.empty(worst * n_q * head_dim, dtype=torch.float32, device=device)
         self.part_ml = torch.empty(worst * n_q * 2, dtype=torch.float32, device=device)
         self.n_q, self.head_dim = n_q, head_dim
+        self.status = torch.zeros(8, dtype=torch.int32, device=device)
+        self.arange = torch.arange(max_rows, dtype=torch.int32, device=device)
+        self.ones = torch.ones(max_rows, dtype=torch.int32, device=device)
+        self.num_sms = num_sms
+        self.max_splits = max_splits
 
 
 def split_plan(n_rows: int, n_kv: int, max_len: int, num_sms: int = 148,
@@ -79,18 +96,39 @@ def split_plan(n_rows: int, n_kv: int, max_len: int, num_sms: int = 148,
     return kps, n
 
 
+def tc_supported(n_q: int, n_kv: int, d: int, softcap: float = 0.0) -> bool:
+    return softcap == 0.0 and d in (64, 128, 256) and n_q % n_kv == 0 and n_q // n_kv <= 128
+
+
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                     block_table: torch.Tensor, seq_lens: torch.Tensor, ws: AttentionWorkspace,
                     out: torch.Tensor, max_len: int, scale: float, window: int = 0,
                     sinks: torch.Tensor | None = None, softcap: float = 0.0,
                     tree_mask: torch.Tensor | None = None, tree_start: torch.Tensor | None = None,
-                    num_sms: int = 148):
+                    num_sms: int = 148, groups=None, force_simt: bool = False):
     """q [T, n_q, d] fp16 -> out [T, n_q, d] fp16 over paged K/V.
 
     Row t sees keys [0, seq_lens[t]) of its block table row (minus the
-    sliding window, plus the tree mask for keys at/after tree_start[t])."""
+    sliding window, plus the tree mask for keys at/after tree_start[t]).
+    `groups` = (row0 int32[G], npos int32[G], positions_per_group): runs of
+    consecutive positions of one sequence that share a CTA on the tensor-core
+    path (prefill chunks, tree rows); None = every row alone (decode)."""
     T, n_q, d = q.shape
     n_kv = k_cache.shape[1]
+    if not force_simt and tc_supported(n_q, n_kv, d, softcap):
+        if groups is None:
+            groups = (ws.arange[:T], ws.ones[:T], 1)
+        row0, npos, ppg = groups
+        G = row0.shape[0]
+        if ppg > 1:  # multi-position groups (prefill/tree): no key splits
+            kps, ns = (max_len + 127) // 128 * 128, 1
+        else:
+            kps, ns = tc_split_plan(G, n_kv, max_len, num_sms, ws.max_splits)
+        part_o = ws.part_o[: T * n_q * ns * d].view(T, n_q, ns, d)
+        part_ml = ws.part_ml[: T * n_q * ns * 2].view(T, n_q, ns, 2)
+        C().attn_tc(q, k_cache, v_cache, row0, npos, ppg, block_table, seq_lens, tree_mask,
+                    tree_start, sinks, window, scale, kps, ns, out, part_o, part_ml, ws.status)
+        return
     kps, ns = split_plan(T, n_kv, max_len, num_sms, ws.max_splits)
     part_o = ws.part_o[: T * n_q * ns * d].view(T, n_q, ns, d)
     part_ml = ws.part_ml[: T * n_q * ns * 2].view(T, n_q, ns, 2)

@@ -224,9 +224,10 @@ def _attn_ref(q, K, V, bt, lens, ps, scale, window=0, sinks=None, tmask=None, ts
     return out
 
 
+@pytest.mark.parametrize("force_simt", [False, True])
 @pytest.mark.parametrize("d,nq,nkv", [(128, 64, 8), (128, 24, 8), (64, 64, 8), (256, 16, 2)])
 @pytest.mark.parametrize("window,sinks", [(0, False), (128, True)])
-def test_paged_decode_attention(d, nq, nkv, window, sinks):
+def test_paged_decode_attention(d, nq, nkv, window, sinks, force_simt):
     from swarmllm_b200.ops.attention import AttentionWorkspace, paged_attention
     torch.manual_seed(0)
     ps, P = 16, 64
@@ -241,8 +242,45 @@ def test_paged_decode_attention(d, nq, nkv, window, sinks):
     ws = AttentionWorkspace(DEV, T, nq, nkv, d, 768)
     out = torch.empty(T, nq, d, dtype=torch.float16, device=DEV)
     paged_attention(q.to(DEV), K.to(DEV), V.to(DEV), bt.to(DEV), lens.to(DEV), ws, out, 768, scale,
-                    window, sk.to(DEV) if sinks else None)
+                    window, sk.to(DEV) if sinks else None, force_simt=force_simt)
+    torch.cuda.synchronize()
+    assert int(ws.status[0]) == 0, ws.status.tolist()
     ref = _attn_ref(q, K, V, bt, lens, ps, scale, window, sk)
+    assert rel_err(out.double().cpu(), ref) < 3e-3
+
+
+@pytest.mark.parametrize("d,nq,nkv,window", [(128, 64, 8, 0), (128, 24, 8, 0), (64, 64, 8, 128),
+                                             (256, 16, 2, 0)])
+def test_attention_prefill_groups(d, nq, nkv, window):
+    """Chunked prefill on the tensor-core path: rows of one sequence grouped
+    128 // n_rep positions per CTA, causal lengths, a prefix already cached."""
+    from swarmllm_b200.engine.runner import attention_groups
+    from swarmllm_b200.ops.attention import AttentionWorkspace, paged_attention
+    torch.manual_seed(2)
+    ps, P = 16, 64
+    prefix, chunk = 100, 150          # sequence 0: 100 cached + 150 new rows
+    dec_len = 333                     # sequence 1: one decode row
+    T = chunk + 1
+    K = torch.randn(P, nkv, ps, d).half()
+    V = torch.randn(P, nkv, ps, d).half()
+    bt0 = torch.randperm(P)[:32].int()
+    bt1 = torch.randperm(P)[:32].int()
+    bt = torch.cat([bt0[None].repeat(chunk, 1), bt1[None]], 0)
+    lens = torch.cat([torch.arange(prefix + 1, prefix + chunk + 1), torch.tensor([dec_len])]).int()
+    q = torch.randn(T, nq, d).half()
+
+    class _Plan:
+        seq_start = np.array([0, chunk])
+        seq_ntok = np.array([chunk, 1])
+    r0, npos, ppg = attention_groups(_Plan, nq // nkv)
+    ws = AttentionWorkspace(DEV, T, nq, nkv, d, 512)
+    out = torch.empty(T, nq, d, dtype=torch.float16, device=DEV)
+    paged_attention(q.to(DEV), K.to(DEV), V.to(DEV), bt.to(DEV), lens.to(DEV), ws, out, 512,
+                    1 / math.sqrt(d), window,
+                    groups=(torch.from_numpy(r0).to(DEV), torch.from_numpy(npos).to(DEV), ppg))
+    torch.cuda.synchronize()
+    assert int(ws.status[0]) == 0, ws.status.tolist()
+    ref = _attn_ref(q, K, V, bt, lens, ps, 1 / math.sqrt(d), window)
     assert rel_err(out.double().cpu(), ref) < 3e-3
 
 
