@@ -161,6 +161,23 @@ class LLMEngine:
         self.steps += 1
         return out
 
+    def embed_text(self, ids: list[int]) -> list[float]:
+        """Mean-pooled, L2-normalised input embeddings of a token list (the
+        /v1/embeddings route)."""
+        if not ids:
+            return [0.0] * self.cfg.hidden
+        m = self.model
+        if self.device.type == "cuda":
+            from ..utils.ext import C
+            t = torch.tensor(ids, dtype=torch.int32, device=self.device)
+            out = torch.empty(len(ids), self.cfg.hidden, dtype=torch.float32, device=self.device)
+            C().embed_gather(m.embd, m.embd_type, self.cfg.hidden, t, out)
+            v = out.mean(0)
+        else:
+            v = m.embd[torch.tensor(ids)].float().mean(0)
+        v = v / (v.norm() + 1e-12)
+        return v.cpu().tolist()
+
     def output(self, rid: int) -> list[int]:
         return [int(t) for t in self.sched.output(rid)]
 

@@ -1,0 +1,196 @@
+"""Tokenizers built from GGUF vocab metadata, plus a byte-level fallback.
+
+* ``BPETokenizer``   GPT-2 style byte-level BPE (``tokenizer.ggml.model ==
+                     "gpt2"``: Llama-3, Qwen, gpt-oss): tokens + merges ranks.
+* ``SPMTokenizer``   SentencePiece-style unigram/BPE by scores
+                     (``tokenizer.ggml.model == "llama"``): greedy
+                     highest-score merge of "▁"-prefixed pieces, byte fallback.
+* ``ByteTokenizer``  1 byte = 1 token id (+ offset), for random-init models
+                     whose GGUF carries no vocabulary.
+
+Reference: src/inference/tokenizer.rs:160,603,712,810 (BPE, SPM, Gemma-4).
+The benchmarks feed token ids directly; tokenizers serve the HTTP API.
+"""
+from __future__ import annotations
+
+import re
+
+
+def _bytes_to_unicode() -> dict[int, str]:
+    """The reversible byte -> printable-unicode map of byte-level BPE
+    (published with GPT-2)."""
+    bs = list(range(ord("!"), ord("~") + 1)) + list(range(ord("¡"), ord("¬") + 1)) + \
+        list(range(ord("®"), ord("ÿ") + 1))
+    cs = bs[:]
+    n = 0
+    for b in range(256):
+        if b not in bs:
+            bs.append(b)
+            cs.append(256 + n)
+            n += 1
+    return dict(zip(bs, (chr(c) for c in cs)))
+
+
+class ByteTokenizer:
+    def __init__(self, vocab_size: int = 32000, offset: int = 3, bos_id: int = 1, eos_id: int = 2):
+        self.vocab_size, self.offset = vocab_size, offset
+        self.bos_id, self.eos_id = bos_id, eos_id
+
+    def encode(self, text: str, add_bos: bool = True) -> list[int]:
+        ids = [b + self.offset for b in text.encode("utf-8")]
+        return ([self.bos_id] if add_bos else []) + ids
+
+    def decode(self, ids) -> str:
+        bs = bytes(int(i) - self.offset for i in ids if self.offset <= int(i) < self.offset + 256)
+        return bs.decode("utf-8", errors="replace")
+
+    def token_str(self, i: int) -> str:
+        return self.decode([i])
+
+
+class BPETokenizer:
+    # Llama-3 / GPT-4-style pre-tokenizer split (letters, numbers, punctuation, spaces)
+    PAT = re.compile(r"""'(?:[sdmt]|ll|ve|re)| ?[^\W\d_]+| ?\d{1,3}| ?[^\s\w]+[\r\n]*|\s*[\r\n]+|\s+(?!\S)|\s+""",
+                     re.UNICODE)
+
+    def __init__(self, tokens: list[str], merges: list[str], bos_id: int = -1, eos_id: int = -1,
+                 token_types: list[int] | None = None):
+        self.tokens = tokens
+        self.vocab = {t: i for i, t in enumerate(tokens)}
+        self.ranks = {}
+        for r, m in enumerate(merges):
+            a, _, b = m.partition(" ")
+            self.ranks[(a, b)] = r
+        self.b2u = _bytes_to_unicode()
+        self.u2b = {v: k for k, v in self.b2u.items()}
+        self.bos_id, self.eos_id = bos_id, eos_id
+        self.special = {t: i for i, t in enumerate(tokens)
+                        if token_types and token_types[i] in (3, 4)}  # control / user-defined
+        self._cache: dict[str, list[int]] = {}
+        self.vocab_size = len(tokens)
+
+    def _bpe(self, word: str) -> list[int]:
+        if word in self._cache:
+            return self._cache[word]
+        parts = list(word)
+        while len(parts) > 1:
+            best, bi = None, -1
+            for i in range(len(parts) - 1):
+                r = self.ranks.get((parts[i], parts[i + 1]))
+                if r is not None and (best is None or r < best):
+                    best, bi = r, i
+            if best is None:
+                break
+            parts[bi:bi + 2] = [parts[bi] + parts[bi + 1]]
+        ids = []
+        for p in parts:
+            if p in self.vocab:
+                ids.append(self.vocab[p])
+            else:  # unknown piece: fall back to its bytes
+                ids.extend(self.vocab.get(ch, 0) for ch in p)
+        self._cache[word] = ids
+        return ids
+
+    def encode(self, text: str, add_bos: bool = True) -> list[int]:
+        ids = [self.bos_id] if (add_bos and self.bos_id >= 0) else []
+        # split out special tokens first
+        if self.special:
+            pat = "(" + "|".join(re.escape(s) for s in sorted(self.special, key=len, reverse=True)) + ")"
+            chunks = re.split(pat, text)
+        else:
+            chunks = [text]
+        for ch in chunks:
+            if not ch:
+                continue
+            if ch in self.special:
+                ids.append(self.special[ch])
+                continue
+            for w in self.PAT.findall(ch):
+                ids.extend(self._bpe("".join(self.b2u[b] for b in w.encode("utf-8"))))
+        return ids
+
+    def decode(self, ids) -> str:
+        out = bytearray()
+        for i in ids:
+            i = int(i)
+            if i < 0 or i >= len(self.tokens) or i in (self.bos_id, self.eos_id):
+                continue
+            t = self.tokens[i]
+            if t in self.special:
+                out += t.encode()
+                continue
+            for ch in t:
+                b = self.u2b.get(ch)
+                if b is not None:
+                    out.append(b)
+                else:
+                    out += ch.encode()
+        return out.decode("utf-8", errors="replace")
+
+    def token_str(self, i: int) -> str:
+        return self.decode([i])
+
+
+class SPMTokenizer:
+    def __init__(self, tokens: list[str], scores: list[float], bos_id: int = 1, eos_id: int = 2):
+        self.tokens, self.scores = tokens, scores
+        self.vocab = {t: i for i, t in enumerate(tokens)}
+        self.bos_id, self.eos_id = bos_id, eos_id
+        self.byte_ids = {}
+        for i, t in enumerate(tokens):
+            m = re.fullmatch(r"<0x([0-9A-Fa-f]{2})>", t)
+            if m:
+                self.byte_ids[int(m.group(1), 16)] = i
+        self.vocab_size = len(tokens)
+
+    def encode(self, text: str, add_bos: bool = True) -> list[int]:
+        text = "▁" + text.replace(" ", "▁")
+        parts = list(text)
+        while True:
+            best, bi = None, -1
+            for i in range(len(parts) - 1):
+                cand = parts[i] + parts[i + 1]
+                j = self.vocab.get(cand)
+                if j is not None and (best is None or self.scores[j] > best):
+                    best, bi = self.scores[j], i
+            if best is None:
+                break
+            parts[bi:bi + 2] = [parts[bi] + parts[bi + 1]]
+        ids = [self.bos_id] if add_bos else []
+        for p in parts:
+            if p in self.vocab:
+                ids.append(self.vocab[p])
+            else:
+                ids.extend(self.byte_ids.get(b, 0) for b in p.encode("utf-8"))
+        return ids
+
+    def decode(self, ids) -> str:
+        out = bytearray()
+        for i in ids:
+            i = int(i)
+            if i in (self.bos_id, self.eos_id) or not (0 <= i < len(self.tokens)):
+                continue
+            t = self.tokens[i]
+            m = re.fullmatch(r"<0x([0-9A-Fa-f]{2})>", t)
+            if m:
+                out.append(int(m.group(1), 16))
+            else:
+                out += t.replace("▁", " ").encode()
+        s = out.decode("utf-8", errors="replace")
+        return s[1:] if s.startswith(" ") else s
+
+    def token_str(self, i: int) -> str:
+        return self.decode([i])
+
+
+def from_gguf_metadata(md: dict, vocab_size: int):
+    model = md.get("tokenizer.ggml.model")
+    toks = md.get("tokenizer.ggml.tokens")
+    bos = int(md.get("tokenizer.ggml.bos_token_id", -1))
+    eos = int(md.get("tokenizer.ggml.eos_token_id", -1))
+    if toks and model == "gpt2":
+        return BPETokenizer(toks, md.get("tokenizer.ggml.merges", []), bos, eos,
+                            md.get("tokenizer.ggml.token_type"))
+    if toks and model == "llama":
+        return SPMTokenizer(toks, md.get("tokenizer.ggml.scores", [0.0] * len(toks)), bos, eos)
+    return ByteTokenizer(vocab_size)

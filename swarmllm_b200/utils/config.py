@@ -1,0 +1,65 @@
+"""Engine configuration from a TOML file and SWARMLLM_* environment variables.
+
+The reference keeps its inference flags in a TOML [inference] section
+(config/default.toml:10-172; src/config/inference.rs:19-686) with env
+overrides.  Names kept where the meaning matches:
+
+  [inference]
+  continuous_batching = true      (always on here)
+  prefill_chunk_tokens = 2048     -> EngineConfig.prefill_chunk
+  max_concurrent_decode_batch     -> EngineConfig.max_running
+  max_seq_len_override            -> EngineConfig.max_model_len
+  prefix_cache_enabled            -> EngineConfig.prefix_cache
+  cuda_graphs (SWARMLLM_CUDA_GRAPH=0 disables)
+
+Environment: SWARMLLM_MAX_MODEL_LEN, SWARMLLM_MAX_RUNNING, SWARMLLM_PREFILL_CHUNK,
+SWARMLLM_KV_PAGES, SWARMLLM_KV_FRACTION, SWARMLLM_PREFIX_CACHE, SWARMLLM_CUDA_GRAPH.
+"""
+from __future__ import annotations
+
+import os
+
+from ..engine.engine import EngineConfig
+
+_TOML_KEYS = {
+    "prefill_chunk_tokens": "prefill_chunk",
+    "max_concurrent_decode_batch": "max_running",
+    "max_seq_len_override": "max_model_len",
+    "prefix_cache_enabled": "prefix_cache",
+    "max_step_tokens": "max_step_tokens",
+    "kv_pages": "kv_pages",
+    "kv_fraction": "kv_fraction",
+    "cuda_graphs": "cuda_graphs",
+    "page_size": "page_size",
+}
+
+_ENV = {
+    "SWARMLLM_MAX_MODEL_LEN": ("max_model_len", int),
+    "SWARMLLM_MAX_RUNNING": ("max_running", int),
+    "SWARMLLM_PREFILL_CHUNK": ("prefill_chunk", int),
+    "SWARMLLM_MAX_STEP_TOKENS": ("max_step_tokens", int),
+    "SWARMLLM_KV_PAGES": ("kv_pages", int),
+    "SWARMLLM_KV_FRACTION": ("kv_fraction", float),
+    "SWARMLLM_PREFIX_CACHE": ("prefix_cache", lambda v: v not in ("0", "false", "False")),
+    "SWARMLLM_CUDA_GRAPH": ("cuda_graphs", lambda v: v not in ("0", "false", "False")),
+}
+
+
+def load_engine_config(path: str | None = None, env=None) -> EngineConfig:
+    cfg = EngineConfig()
+    if path:
+        import tomllib
+        with open(path, "rb") as f:
+            data = tomllib.load(f)
+        inf = data.get("inference", data)
+        for k, v in inf.items():
+            attr = _TOML_KEYS.get(k)
+            if attr is not None:
+                setattr(cfg, attr, type(getattr(cfg, attr))(v))
+    env = os.environ if env is None else env
+    for k, (attr, conv) in _ENV.items():
+        if k in env:
+            setattr(cfg, attr, conv(env[k]))
+    if cfg.max_step_tokens < cfg.prefill_chunk:
+        cfg.max_step_tokens = cfg.prefill_chunk
+    return cfg

@@ -1,0 +1,50 @@
+"""Prometheus metrics (reference names: src/api/metrics.rs:303-924,
+e.g. swarmllm_inference_requests_total, swarmllm_inference_latency_seconds).
+Each server owns a private registry, so several engines in one process (tests)
+do not collide."""
+from __future__ import annotations
+
+from prometheus_client import CollectorRegistry, Counter, Gauge, Histogram, generate_latest
+
+
+class Metrics:
+    def __init__(self):
+        r = self.registry = CollectorRegistry()
+        self.req_total = Counter("swarmllm_inference_requests_total", "Requests started", registry=r)
+        self.req_done = Counter("swarmllm_inference_requests_completed_total", "Requests completed",
+                                registry=r)
+        self.tokens = Counter("swarmllm_tokens_generated_total", "Tokens generated", registry=r)
+        self.latency = Histogram("swarmllm_inference_latency_seconds", "Request latency", registry=r,
+                                 buckets=(0.05, 0.1, 0.25, 0.5, 1, 2, 5, 10, 30, 60, 120))
+        self.ttft = Histogram("swarmllm_time_to_first_token_seconds", "Time to first token", registry=r,
+                              buckets=(0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1, 2, 5, 10))
+        self.tpot = Histogram("swarmllm_time_per_output_token_seconds", "Mean gap between tokens",
+                              registry=r, buckets=(0.002, 0.005, 0.01, 0.02, 0.05, 0.1, 0.25, 0.5))
+        self.step_s = Histogram("swarmllm_engine_step_seconds", "Engine step time", registry=r,
+                                buckets=(0.001, 0.0025, 0.005, 0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1))
+        self.kv_free = Gauge("swarmllm_kv_pages_free", "Free KV pages", registry=r)
+        self.kv_total = Gauge("swarmllm_kv_pages_total", "KV pages", registry=r)
+
+    def requests_started(self):
+        self.req_total.inc()
+
+    def step(self, seconds: float, n_tokens: int):
+        self.step_s.observe(seconds)
+        if n_tokens:
+            self.tokens.inc(n_tokens)
+
+    def request_done(self, tr):
+        self.req_done.inc()
+        if tr.t_done is not None:
+            self.latency.observe(tr.t_done - tr.t_arrival)
+        if tr.ttft is not None:
+            self.ttft.observe(tr.ttft)
+        if tr.tpot is not None:
+            self.tpot.observe(tr.tpot)
+
+    def set_kv(self, free: int, total: int):
+        self.kv_free.set(free)
+        self.kv_total.set(total)
+
+    def render(self) -> str:
+        return generate_latest(self.registry).decode()
