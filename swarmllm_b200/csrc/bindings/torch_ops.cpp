@@ -1,50 +1,7 @@
 // PyTorch bindings for the sm_100a kernels (module swarmllm_b200._C).
 // Every op launches on torch's current CUDA stream, so they can be captured in
 // CUDA graphs.  Shapes and dtypes are checked here; the kernels trust them.
-#include <torch/extension.h>
-#include <ATen/cuda/CUDAContext.h>
-#include <c10/cuda/CUDAGuard.h>
-#include <execinfo.h>
-#include <signal.h>
-#include <unistd.h>
-
-#include <cstdlib>
-
-#include "kernels.h"
-#include "gemm_out.cuh"
-
-namespace py = pybind11;
-using at::Tensor;
-using OptT = std::optional<Tensor>;
-
-#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
-#define CHECK_CONTIG(x) TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
-#define CHECK_DT(x, dt) TORCH_CHECK((x).scalar_type() == (dt), #x " has wrong dtype")
-
-static cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
-
-template <typename T>
-static T* ptr_or_null(const OptT& t) {
-  return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
-}
-
-// A GEMM result: the fp32 workspace plus how to read it (see gemm_out.cuh).
-struct GemmResult {
-  swarm::GemmOut g{};
-  Tensor ws;  // keeps the buffer alive
-};
-
-static int num_sms_of(const Tensor& t) {
-  static int cached[64] = {0};
-  int dev = t.get_device();
-  if (dev < 0 || dev >= 64) dev = 0;
-  if (!cached[dev]) {
-    cudaDeviceProp p;
-    cudaGetDeviceProperties(&p, dev);
-    cached[dev] = p.multiProcessorCount;
-  }
-  return cached[dev];
-}
+#include "ops_common.h"
 
 // ---------------------------------------------------------------- elementwise
 void embed_gather(Tensor table, int64_t type, int64_t hidden, Tensor ids, Tensor out) {
@@ -262,6 +219,8 @@ static void segv_handler(int sig) {
   raise(sig);
 }
 
+void register_moe_ops(py::module& m);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "swarmllm_b200 sm_100a kernels";
   if (const char* e = getenv("SWARMLLM_SEGV_BT")) {
@@ -292,4 +251,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax);
   m.def("sample", &sample);
   m.def("philox_uniform", &philox_uniform);
+  register_moe_ops(m);
 }

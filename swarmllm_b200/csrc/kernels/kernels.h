@@ -74,3 +74,30 @@ void launch_sample(const float* logits, int rows, int V, int stride, const float
                    const int32_t* positions, int32_t* out, cudaStream_t s);
 void launch_philox_uniform(uint64_t seed, const int32_t* positions, int n_pos, int V, float* out,
                            cudaStream_t s);
+
+// ---- mixture of experts (moe_tc.cu) -----------------------------------------
+// fmt: 0 = Q4_K experts (fp16 activations), 1 = MXFP4 experts (bf16 activations)
+// epi: 0 = SwiGLU (gate/up rows interleaved in groups of 16) -> 16-bit H
+//      1 = store fp32 rows to out_ptrs[ret >> 24][ret & 0xFFFFFF]
+int moe_tok_tile(int pairs, int n_experts);
+int moe_max_tiles(int pairs, int n_experts, int tok_tile);
+long long moe_packed_bytes(int fmt, int rows, int K);
+int launch_mxfp4_repack(const void* src, int rows, int K, void* dst, cudaStream_t s);
+int launch_moe_route(const __half* x, int x_stride, int T, int H, const void* wr, int wtype,
+                     const float* br, int E, int k, int softmax_after_topk, int32_t* ids,
+                     float* wts, int* counts, cudaStream_t s);
+int launch_moe_plan(int* counts, int E, int tok_tile, int* offsets, int* cursor, void* tiles,
+                    int* n_tiles, int max_tiles, int* status, cudaStream_t s);
+int launch_moe_scatter(const __half* x, int x_stride, int H, const int32_t* ids, int P, int k,
+                       int* cursor, void* xs, int xs_stride, int xs_bf16, int32_t* ret,
+                       int rank, cudaStream_t s);
+int launch_moe_gemm_tc(int fmt, int epi, const void* w, int rows, int K, const void* xs,
+                       int xs_stride, int xs_rows, int tok_tile, const void* tiles,
+                       const int* n_tiles, int max_tiles, const float* bias, int bias_stride,
+                       void* h, int h_stride, int act_kind, float alpha, float limit,
+                       const unsigned long long* out_ptrs, int n_out, int out_stride,
+                       const int32_t* ret, int num_sms, int* status, cudaStream_t s);
+int launch_moe_combine(const float* rows, int row_stride, const float* wts, int k,
+                       const swarm::GemmOut* sh, const swarm::GemmOut* shg, float* residual,
+                       int T, int H, const float* norm_w, __half* out, int out_stride, float eps,
+                       cudaStream_t s);

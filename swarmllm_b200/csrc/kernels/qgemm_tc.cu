@@ -33,12 +33,12 @@
 // tile segment.
 #include "kernels.h"
 #include "gemm_out.cuh"
+#include "qgemm_common.cuh"
 #include "tc_utils.cuh"
 
 namespace swarm {
 using namespace tc;
 
-constexpr int kQ4kRowBytes = 144;
 constexpr int kWStageBytes = 128 * kQ4kRowBytes;  // 18432
 constexpr int kTmemCols = 512;
 
@@ -85,61 +85,6 @@ struct QGemmArgs {
     if ((tr) != nullptr && blockIdx.x == 0 && (unit) < 512) (tr)[(unit) * 8 + (ev)] = \
         globaltimer();                                                                 \
   } while (0)
-
-SW_DEVICE __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-SW_DEVICE uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-
-// 8 permuted nibbles -> 4 fp16 pairs (K order), scale s, min mb.
-SW_DEVICE void dq_word(uint32_t x, __half2 S, __half2 S16, __half2 MB, uint32_t* out) {
-  const uint32_t MAGIC = 0x64006400u;
-  const __half2 K1024 = u32_as_h2(0x64006400u);
-  const uint32_t hi = x >> 8;
-  __half2 c0 = __hsub2(u32_as_h2((x & 0x000F000Fu) | MAGIC), K1024);
-  __half2 c1 = __hsub2(u32_as_h2((x & 0x00F000F0u) | MAGIC), K1024);
-  __half2 c2 = __hsub2(u32_as_h2((hi & 0x000F000Fu) | MAGIC), K1024);
-  __half2 c3 = __hsub2(u32_as_h2((hi & 0x00F000F0u) | MAGIC), K1024);
-  out[0] = h2_as_u32(__hfma2(c0, S, MB));
-  out[1] = h2_as_u32(__hfma2(c1, S16, MB));
-  out[2] = h2_as_u32(__hfma2(c2, S, MB));
-  out[3] = h2_as_u32(__hfma2(c3, S16, MB));
-}
-
-// (d*sc_j, dmin*m_j) for the 8 sub-blocks from the 16-byte header
-// {f16 d, f16 dmin, u8 scales[12]}; constant byte indices keep it in registers.
-SW_DEVICE void q4k_decode_scales(const uint4& hdr, float* s, float* mb) {
-  const float d = half_bits_to_f((uint16_t)(hdr.x & 0xFFFF));
-  const float dmin = half_bits_to_f((uint16_t)(hdr.x >> 16));
-  const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;
-#define SB(i) ((int)((((i) < 4 ? w0 : ((i) < 8 ? w1 : w2)) >> (8 * ((i) & 3))) & 0xFF))
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    int sc, m;
-    if (j < 4) {
-      sc = SB(j) & 63;
-      m = SB(j + 4) & 63;
-    } else {
-      sc = (SB(j + 4) & 0xF) | ((SB(j - 4) >> 6) << 4);
-      m = (SB(j + 4) >> 4) | ((SB(j) >> 6) << 4);
-    }
-    s[j] = d * (float)sc;
-    mb[j] = dmin * (float)m;
-  }
-#undef SB
-}
-
-// Dequantize one row's superblock (256 K values) into the unit's 128 TMEM columns.
-SW_DEVICE void dq_unit(const uint4 (&q)[8], const float* sc, const float* mb, uint32_t taddr) {
-  const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
-#pragma unroll
-  for (int sub = 0; sub < 8; ++sub) {
-    const __half2 S = __float2half2_rn(sc[sub]), S16 = __float2half2_rn(sc[sub] * 0.0625f);
-    const __half2 MB = __float2half2_rn(-mb[sub]);
-    uint32_t cols[16];
-#pragma unroll
-    for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[4 * sub + w4], S, S16, MB, cols + 4 * w4);
-    tmem_st_x16(taddr + sub * 16, cols);
-  }
-}
 
 template <int N>
 __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)

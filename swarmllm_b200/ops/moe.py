@@ -1,0 +1,147 @@
+"""Mixture-of-experts FFN on the GPU: routing, dispatch, grouped expert GEMMs
+on the tensor cores, combine (kernels in csrc/kernels/moe_tc.cu).
+
+One MoE layer is six launches, all sized from host-side bounds so the whole
+layer can be captured in a CUDA graph (the per-expert token counts stay on
+the device):
+
+    moe_route    router GEMV + bias + top-k + routing weights + expert counts
+    moe_plan     per-expert offsets and the (expert, token-tile) tile list
+    moe_scatter  token rows -> expert-sorted rows (fp16 for Q4_K experts,
+                 bf16 for MXFP4 experts), destination slot per row
+    moe_gemm     gate|up grouped GEMM, SwiGLU epilogue -> H
+    moe_gemm     down grouped GEMM, (+bias) rows stored at their (rank, slot)
+    moe_combine  weighted sum over the k rows of a token (+ gated shared
+                 expert), residual add, next RMSNorm
+
+Reference: MoeFfn (src/inference/layers/moe.rs), expert GEMM kernels
+vendor/candle/candle-kernels/src/moe/moe_gguf.cu:56 and moe_wmma_gguf.cu:191.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..gguf import quants as Q
+from ..utils.ext import C
+
+FMT_Q4K, FMT_MXFP4 = 0, 1
+EPI_SWIGLU, EPI_STORE = 0, 1
+
+
+def _fmt_of(qtype: int) -> int:
+    if qtype == Q.Q4_K:
+        return FMT_Q4K
+    if qtype == Q.MXFP4:
+        return FMT_MXFP4
+    raise NotImplementedError(f"expert weights of type {Q.TYPE_NAMES.get(qtype, qtype)}: the "
+                              "grouped tensor-core GEMM takes Q4_K or MXFP4 experts")
+
+
+def _repack(raw: torch.Tensor, fmt: int, rows: int, K: int, dev) -> torch.Tensor:
+    """raw [E, rows, row_bytes] uint8 (GGUF blocks) -> packed [E, bytes] uint8."""
+    E = raw.shape[0]
+    nb = int(C().moe_packed_bytes(fmt, rows, K))
+    out = torch.empty(E, nb, dtype=torch.uint8, device=dev)
+    for e in range(E):
+        if fmt == FMT_Q4K:
+            C().q4k_repack(raw[e].contiguous(), rows, K, out[e])
+        else:
+            C().mxfp4_repack(raw[e].contiguous(), rows, K, out[e])
+    return out
+
+
+class MoeExperts:
+    """Packed weights of one layer's experts (all of them, or the local slice
+    [e0, e0 + n_local) under expert parallelism).
+
+    gate|up rows are interleaved in groups of 16 (16 gate rows, then the
+    matching 16 up rows) so that one warp of the GEMM epilogue holds both
+    halves of a feature and applies the SwiGLU with one shuffle."""
+
+    def __init__(self, gate, up, down, qtype: int, H: int, F: int, dev, e0: int = 0,
+                 n_local: int | None = None, gate_b=None, up_b=None, down_b=None,
+                 act_kind: int = 0, alpha: float = 1.702, limit: float = 7.0):
+        assert F % 64 == 0, "expert FFN width must be a multiple of 64"
+        self.fmt = _fmt_of(qtype)
+        self.H, self.F = H, F
+        E = gate.shape[0]
+        n_local = E if n_local is None else n_local
+        self.e0, self.n_local = e0, n_local
+        sl = slice(e0, e0 + n_local)
+        rb_in = Q.nbytes(qtype, H)
+        g = gate[sl].to(dev).reshape(n_local, F // 16, 16, rb_in)
+        u = up[sl].to(dev).reshape(n_local, F // 16, 16, rb_in)
+        gu = torch.stack([g, u], dim=2).reshape(n_local, 2 * F, rb_in)
+        self.w_gu = _repack(gu, self.fmt, 2 * F, H, dev)
+        d = down[sl].to(dev).reshape(n_local, H, Q.nbytes(qtype, F))
+        self.w_down = _repack(d, self.fmt, H, F, dev)
+        self.b_gu = None
+        if gate_b is not None:
+            bg = gate_b[sl].reshape(n_local, F // 16, 16)
+            bu = up_b[sl].reshape(n_local, F // 16, 16)
+            self.b_gu = torch.stack([bg, bu], dim=2).reshape(n_local, 2 * F).float().to(dev).contiguous()
+        self.b_down = down_b[sl].float().to(dev).contiguous() if down_b is not None else None
+        self.act_kind, self.alpha, self.limit = act_kind, alpha, limit
+        self.x_dtype = torch.bfloat16 if self.fmt == FMT_MXFP4 else torch.float16
+
+    @property
+    def nbytes(self) -> int:
+        return self.w_gu.numel() + self.w_down.numel()
+
+
+class MoeWorkspace:
+    """Routing and dispatch buffers for up to `max_tokens` tokens."""
+
+    def __init__(self, dev, max_tokens: int, H: int, F: int, E: int, k: int, x_dtype,
+                 num_sms: int, max_pairs: int | None = None):
+        self.E, self.k, self.H, self.F = E, k, H, F
+        P = max_pairs or max_tokens * k
+        self.P = P
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.ids = torch.zeros(max_tokens * k, **i32)
+        self.wts = torch.zeros(max_tokens * k, dtype=torch.float32, device=dev)
+        self.counts = torch.zeros(E, **i32)  # kept zero between layers by moe_plan
+        self.offsets = torch.zeros(E + 1, **i32)
+        self.cursor = torch.zeros(E, **i32)
+        self.max_tiles = int(C().moe_max_tiles(P, E, 16))
+        self.tiles = torch.zeros(self.max_tiles, 4, **i32)
+        self.n_tiles = torch.zeros(1, **i32)
+        self.ret = torch.zeros(P, **i32)
+        self.xs = torch.zeros(P, H, dtype=x_dtype, device=dev)
+        self.h = torch.zeros(P, F, dtype=x_dtype, device=dev)
+        self.rows = torch.zeros(max_tokens * k, H, dtype=torch.float32, device=dev)
+        self.status = torch.zeros(8, **i32)
+        self.num_sms = num_sms
+
+    def check(self):
+        s = self.status.cpu().tolist()
+        if s[0]:
+            raise RuntimeError(f"MoE kernel reported a timed-out wait: code {s[0]} block {s[1]} "
+                               f"detail {s[2]},{s[3]}")
+        if s[6]:
+            raise RuntimeError(f"MoE tile list overflow: {s[6]} tiles")
+
+
+def moe_ffn(x: torch.Tensor, experts: MoeExperts, router_w: torch.Tensor, router_type: int,
+            router_b: torch.Tensor | None, ws: MoeWorkspace, residual: torch.Tensor,
+            norm_w: torch.Tensor | None, out: torch.Tensor | None, eps: float,
+            softmax_after_topk: bool = True, shared=None, shared_gate=None):
+    """residual += MoE(x) (+ shared); out = RMSNorm(residual) * norm_w when out
+    is given.  x: fp16 [T, H] normed activations."""
+    T = x.shape[0]
+    E, k = ws.E, ws.k
+    P = T * k
+    c = C()
+    c.moe_route(x, router_w, router_type, router_b, E, k, softmax_after_topk, ws.ids, ws.wts,
+                ws.counts)
+    N = int(c.moe_tok_tile(P, E))
+    c.moe_plan(ws.counts, E, N, ws.offsets, ws.cursor, ws.tiles, ws.n_tiles, ws.status)
+    c.moe_scatter(x, ws.ids[:P], k, ws.cursor, ws.xs, ws.ret, 0)
+    ex = experts
+    c.moe_gemm(ex.fmt, EPI_SWIGLU, ex.w_gu, 2 * ex.F, ex.H, ws.xs, N, ws.tiles, ws.n_tiles,
+               ex.b_gu, 2 * ex.F, ws.h, ex.act_kind, ex.alpha, ex.limit, [], 0, None,
+               ws.num_sms, ws.status)
+    c.moe_gemm(ex.fmt, EPI_STORE, ex.w_down, ex.H, ex.F, ws.h, N, ws.tiles, ws.n_tiles,
+               ex.b_down, ex.H, None, 0, 0.0, 0.0, [ws.rows.data_ptr()], ex.H, ws.ret,
+               ws.num_sms, ws.status)
+    c.moe_combine(ws.rows, ws.wts, k, shared, shared_gate, residual, norm_w, out, eps)
