@@ -111,6 +111,33 @@ GemmResult qgemm_q4k_tc(Tensor w_packed, int64_t rows, int64_t K, Tensor x, Tens
   return r;
 }
 
+GemmResult dense_gemm_tc(Tensor w, Tensor x, Tensor ws, Tensor status, int64_t num_sms) {
+  CHECK_DT(w, at::kHalf); CHECK_DT(x, at::kHalf); CHECK_DT(ws, at::kFloat);
+  CHECK_DT(status, at::kInt);
+  TORCH_CHECK(status.numel() >= 8, "status must hold 8 ints");
+  TORCH_CHECK(w.dim() == 2 && w.stride(1) == 1 && x.stride(-1) == 1, "row-major operands");
+  TORCH_CHECK(x.size(-1) == w.size(1), "K mismatch");
+  const at::cuda::CUDAGuard guard(x.device());
+  if (num_sms <= 0) num_sms = num_sms_of(x);
+  GemmResult r;
+  int rc = launch_dense_gemm_tc(reinterpret_cast<const __half*>(w.data_ptr()), (int)w.size(0),
+                                (int)w.size(1), (int)w.stride(0),
+                                reinterpret_cast<const __half*>(x.data_ptr()), (int)x.stride(0),
+                                (int)x.size(0), ws.data_ptr<float>(), (size_t)ws.numel(),
+                                (int)num_sms, status.data_ptr<int>(), &r.g, cur_stream());
+  TORCH_CHECK(rc == 0, "dense_gemm_tc launch failed: rc=", rc);
+  r.ws = ws;
+  return r;
+}
+
+py::tuple dense_tc_plan_py(int64_t rows, int64_t K, int64_t T, int64_t num_sms) {
+  int N, ntt, kb, upc, ctas;
+  long total;
+  size_t need;
+  dense_tc_plan((int)rows, (int)K, (int)T, (int)num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need);
+  return py::make_tuple(N, ntt, kb, total, upc, ctas, need);
+}
+
 void qgemm_set_trace_py(OptT buf) {
   if (buf.has_value()) TORCH_CHECK(buf->numel() * buf->element_size() >= 512 * 8 * 8, "trace buffer too small");
   qgemm_set_trace(ptr_or_null<void>(buf));
@@ -244,6 +271,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("q4k_tc_plan", &q4k_tc_plan_py);
   m.def("qgemm_q4k_tc", &qgemm_q4k_tc);
   m.def("q4k_repack", &q4k_repack);
+  m.def("dense_gemm_tc", &dense_gemm_tc);
+  m.def("dense_tc_plan", &dense_tc_plan_py);
   m.def("qgemm_set_trace", &qgemm_set_trace_py);
   m.def("decode_attn", &decode_attn);
   m.def("attn_tc", &attn_tc);

@@ -42,6 +42,12 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
                         int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
                         swarm::GemmOut* out, cudaStream_t s);
 void qgemm_set_trace(void* buf);
+// Dense fp16 weights on tcgen05 (dense_gemm_tc.cu); same workspace contract.
+void dense_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* kb,
+                   long* total_units, int* upc, int* n_ctas, size_t* ws_floats);
+int launch_dense_gemm_tc(const __half* w, int rows, int K, int w_stride, const __half* x,
+                         int x_stride, int T, float* ws, size_t ws_floats_avail, int num_sms,
+                         int* status, swarm::GemmOut* out, cudaStream_t s);
 int launch_q4k_repack(const void* src, int rows, int K, void* dst, cudaStream_t s);
 int make_tmap_2d_16bit(CUtensorMap* map, const void* base, int rows, int cols, int row_stride,
                        int box_rows, int box_cols, int swizzle_bytes);

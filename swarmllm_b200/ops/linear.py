@@ -67,27 +67,40 @@ class QLinear:
         self.device = torch.device(device)
         raw = data if isinstance(data, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(data))
         raw = raw.reshape(-1).to(self.device, dtype=torch.uint8)
-        self.use_tc = (qtype == Q.Q4_K and rows % 128 == 0 and K % 256 == 0 and not force_simt)
-        if self.use_tc:
+        self.kind = "simt"
+        self.w16 = None
+        self.packed = None
+        self.raw = raw
+        if not force_simt and qtype == Q.Q4_K and rows % 128 == 0 and K % 256 == 0:
+            self.kind = "q4k"
             self.packed = torch.empty(rows * (K // 256) * 144, dtype=torch.uint8, device=self.device)
             C().q4k_repack(raw, rows, K, self.packed)
             self.raw = None
-        else:
-            self.raw = raw
-            self.packed = None
+        elif not force_simt and qtype in (Q.F16, Q.BF16) and K % 8 == 0:
+            # 16-bit weights run on the dense tensor-core GEMM in fp16 (exact
+            # for F16; BF16 rounds the mantissa, kept only when no weight
+            # exceeds the fp16 range).
+            src = raw.view(torch.float16 if qtype == Q.F16 else torch.bfloat16).view(rows, K)
+            if qtype == Q.F16 or float(src.float().abs().max()) < 60000.0:
+                self.kind = "dense"
+                self.w16 = src.to(torch.float16).contiguous()
+                self.raw = None
+        self.use_tc = self.kind != "simt"
         self.bias = None
         if bias is not None:
             self.bias = torch.as_tensor(bias, dtype=torch.float32, device=self.device)
 
     @property
     def nbytes(self) -> int:
-        t = self.packed if self.use_tc else self.raw
-        return t.numel()
+        t = {"q4k": self.packed, "dense": self.w16, "simt": self.raw}[self.kind]
+        return t.numel() * t.element_size()
 
     def __call__(self, x: torch.Tensor, ws: GemmWorkspace):
         T = x.shape[0]
-        if self.use_tc:
+        if self.kind == "q4k":
             return C().qgemm_q4k_tc(self.packed, self.rows, self.K, x, ws.ws, ws.status, ws.num_sms)
+        if self.kind == "dense":
+            return C().dense_gemm_tc(self.w16, x, ws.ws, ws.status, ws.num_sms)
         out = ws.dense(T * self.rows)[: T * self.rows].view(T, self.rows)
         return C().qmatmul_simt(self.raw, self.qtype, self.rows, self.K, x, out)
 
