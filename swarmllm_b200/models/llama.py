@@ -28,6 +28,7 @@ import torch
 from ..gguf import quants as Q
 from ..ops.attention import AttentionWorkspace, PagedKVCache, paged_attention
 from ..ops.linear import GemmWorkspace, QLinear
+from ..ops.moe import MoeExperts, MoeWorkspace, moe_ffn
 from ..utils.ext import C
 from .config import ModelConfig, rope_inv_freq
 
@@ -102,10 +103,14 @@ class LlamaGPU:
             L.k_norm = small(b + "attn_k_norm.weight") if cfg.qk_norm else None
             L.sinks = small(b + "attn_sinks.weight") if cfg.attn_sinks else None
             L.window = cfg.sliding_window if cfg.is_swa(i) else 0
-            g, u = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
-            L.wgu = QLinear(torch.cat([g[0], u[0]]), g[1], 2 * cfg.ffn, H, dev)
-            t, qt, shape = get(b + "ffn_down.weight")
-            L.wdown = QLinear(t, qt, shape[0], shape[1], dev)
+            L.experts = None
+            if cfg.n_experts:
+                self._load_moe(L, b, get, small)
+            else:
+                g, u = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
+                L.wgu = QLinear(torch.cat([g[0], u[0]]), g[1], 2 * cfg.ffn, H, dev)
+                t, qt, shape = get(b + "ffn_down.weight")
+                L.wdown = QLinear(t, qt, shape[0], shape[1], dev)
             self.layers.append(L)
         self.next_norm = None
         if self.last:
@@ -117,17 +122,58 @@ class LlamaGPU:
         self.inv_freq = torch.from_numpy(inv).to(dev)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
 
-    def weight_bytes(self) -> int:
-        n = 0
+    def _load_moe(self, L, b, get, small):
+        """Routed experts (+ router, + shared expert) of one layer."""
+        cfg, dev = self.cfg, self.device
+        E, F, H = cfg.n_experts, cfg.expert_ffn, cfg.hidden
+        g, u, d = (get(b + n) for n in ("ffn_gate_exps.weight", "ffn_up_exps.weight",
+                                         "ffn_down_exps.weight"))
+        qt = g[1]
+        rb_h, rb_f = Q.nbytes(qt, H), Q.nbytes(qt, F)
+        biases = {}
+        if cfg.arch == "gpt-oss":
+            biases = dict(gate_b=small(b + "ffn_gate_exps.bias").cpu(),
+                          up_b=small(b + "ffn_up_exps.bias").cpu(),
+                          down_b=small(b + "ffn_down_exps.bias").cpu())
+        L.experts = MoeExperts(g[0].view(E, F, rb_h), u[0].view(E, F, rb_h),
+                               d[0].view(E, H, rb_f), qt, H, F, dev,
+                               act_kind=1 if cfg.swiglu_limit else 0, alpha=cfg.swiglu_alpha,
+                               limit=cfg.swiglu_limit, **biases)
+        del g, u, d
+        t, rq, _ = get(b + "ffn_gate_inp.weight")
+        L.router, L.router_type = t.contiguous(), rq
+        L.router_b = small(b + "ffn_gate_inp.bias") if cfg.arch == "gpt-oss" else None
+        L.sh_gu = L.sh_down = L.sh_gate = None
+        if cfg.shared_expert_ffn:
+            S = cfg.shared_expert_ffn
+            gs, us = get(b + "ffn_gate_shexp.weight"), get(b + "ffn_up_shexp.weight")
+            L.sh_gu = QLinear(torch.cat([gs[0], us[0]]), gs[1], 2 * S, H, dev)
+            t, qt2, shape = get(b + "ffn_down_shexp.weight")
+            L.sh_down = QLinear(t, qt2, shape[0], shape[1], dev)
+            t, qt3, _ = get(b + "ffn_gate_inp_shexp.weight")
+            L.sh_gate = QLinear(t, qt3, 1, H, dev)
+
+    def _linears(self):
         for L in self.layers:
-            n += L.wqkv.nbytes + L.wo.nbytes + L.wgu.nbytes + L.wdown.nbytes
+            yield from (L.wqkv, L.wo)
+            if L.experts is None:
+                yield from (L.wgu, L.wdown)
+            elif L.sh_gu is not None:
+                yield from (L.sh_gu, L.sh_down)
         if self.last:
-            n += self.head.nbytes
+            yield self.head
+
+    def weight_bytes(self) -> int:
+        n = sum(l.nbytes for l in self._linears())
+        for L in self.layers:
+            if L.experts is not None:
+                n += L.experts.nbytes
         return n
 
     def max_gemm_rows(self) -> int:
         c = self.cfg
-        r = max(c.q_dim + 2 * c.kv_dim, 2 * c.ffn, c.hidden)
+        r = max(c.q_dim * (2 if c.attn_output_gate else 1) + 2 * c.kv_dim, 2 * c.ffn, c.hidden,
+                2 * c.shared_expert_ffn)
         if self.last:
             r = max(r, c.vocab)
         return r
@@ -162,15 +208,28 @@ class LlamaGPU:
                             num_sms=ctx.gemm.num_sms, groups=b.groups)
             g = L.wo(ao, ctx.gemm)
             C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
+            if j + 1 < len(self.layers):
+                nxt_w, nxt_out = self.layers[j + 1].attn_norm, x
+            elif self.last:
+                nxt_w, nxt_out = self.out_norm, x
+            else:
+                nxt_w, nxt_out = None, None
+            if L.experts is not None:
+                sh = shg = None
+                if L.sh_gu is not None:
+                    S = cfg.shared_expert_ffn
+                    g = L.sh_gu(x, ctx.gemm)
+                    C().epi_swiglu(g, None, S, 0, False, 0.0, 0.0, ctx.act_sh[:N])
+                    shg = L.sh_gate(x, ctx.gemm, out=ctx.sh_gate[:N])
+                    sh = L.sh_down(ctx.act_sh[:N], ctx.gemm)
+                moe_ffn(x, L.experts, L.router, L.router_type, L.router_b, ctx.moe, h, nxt_w,
+                        nxt_out, cfg.rms_eps, cfg.moe_softmax_after_topk, sh, shg)
+                continue
             g = L.wgu(x, ctx.gemm)
             C().epi_swiglu(g, None, cfg.ffn, 0, False, 0.0, 0.0, act)
             g = L.wdown(act, ctx.gemm)
-            if j + 1 < len(self.layers):
-                C().epi_residual_rmsnorm(g, h, None, self.layers[j + 1].attn_norm, x, cfg.rms_eps)
-            elif self.last:
-                C().epi_residual_rmsnorm(g, h, None, self.out_norm, x, cfg.rms_eps)
-            else:
-                C().epi_residual_rmsnorm(g, h, None, ctx.dummy_norm, None, cfg.rms_eps)
+            C().epi_residual_rmsnorm(g, h, None, nxt_w if nxt_w is not None else ctx.dummy_norm,
+                                     nxt_out, cfg.rms_eps)
         if not self.last:
             return h
         S = b.sample_rows.shape[0]
@@ -200,17 +259,20 @@ class GpuForwardContext:
         self.xs = torch.zeros(max_samples, H, dtype=torch.float16, device=dev)
         self.logits = torch.zeros(max_samples, cfg.vocab, dtype=torch.float32, device=dev)
         self.dummy_norm = torch.ones(H, dtype=torch.float32, device=dev)
+        self.moe = None
+        if cfg.n_experts:
+            ex = next(L.experts for L in model.layers if L.experts is not None)
+            self.moe = MoeWorkspace(dev, max_tokens, H, cfg.expert_ffn, cfg.n_experts,
+                                    cfg.n_experts_used, ex.x_dtype, self.gemm.num_sms)
+            S = max(cfg.shared_expert_ffn, 1)
+            self.act_sh = torch.zeros(max_tokens, S, dtype=torch.float16, device=dev)
+            self.sh_gate = torch.zeros(max_tokens, 1, dtype=torch.float32, device=dev)
         # Size the CUDA-core GEMM scratch up front (graph capture cannot grow it).
         self.gemm.dense(max_tokens * model.max_gemm_rows() if _has_simt(model) else 0)
 
 
 def _has_simt(model: LlamaGPU) -> bool:
-    lins = []
-    for L in model.layers:
-        lins += [L.wqkv, L.wo, L.wgu, L.wdown]
-    if model.last:
-        lins.append(model.head)
-    return any(not l.use_tc for l in lins)
+    return any(not l.use_tc for l in model._linears())
 
 
 # =========================================================================== CPU
@@ -249,7 +311,23 @@ class LlamaCPU:
             L.k_norm = dq(b + "attn_k_norm.weight") if cfg.qk_norm else None
             L.sinks = dq(b + "attn_sinks.weight") if cfg.attn_sinks else None
             L.window = cfg.sliding_window if cfg.is_swa(i) else 0
-            L.wg, L.wu, L.wd = dq(b + "ffn_gate.weight"), dq(b + "ffn_up.weight"), dq(b + "ffn_down.weight")
+            L.moe = bool(cfg.n_experts)
+            if L.moe:
+                gpt = cfg.arch == "gpt-oss"
+                L.wr = dq(b + "ffn_gate_inp.weight")
+                L.br = dq(b + "ffn_gate_inp.bias") if gpt else None
+                L.eg, L.eu, L.ed = (dq(b + n) for n in ("ffn_gate_exps.weight", "ffn_up_exps.weight",
+                                                         "ffn_down_exps.weight"))
+                L.ebg = dq(b + "ffn_gate_exps.bias") if gpt else None
+                L.ebu = dq(b + "ffn_up_exps.bias") if gpt else None
+                L.ebd = dq(b + "ffn_down_exps.bias") if gpt else None
+                L.sg = None
+                if cfg.shared_expert_ffn:
+                    L.sg, L.su, L.sd = (dq(b + n) for n in ("ffn_gate_shexp.weight", "ffn_up_shexp.weight",
+                                                             "ffn_down_shexp.weight"))
+                    L.sgi = dq(b + "ffn_gate_inp_shexp.weight")
+            else:
+                L.wg, L.wu, L.wd = dq(b + "ffn_gate.weight"), dq(b + "ffn_up.weight"), dq(b + "ffn_down.weight")
             self.layers.append(L)
         if self.last:
             self.out_norm = dq("output_norm.weight")
@@ -278,6 +356,40 @@ class LlamaCPU:
             out[..., 0:rd:2] = a * c - b * s
             out[..., 1:rd:2] = b * c + a * s
         return out
+
+    def _act(self, g, u):
+        cfg = self.cfg
+        if not cfg.swiglu_limit:
+            return torch.nn.functional.silu(g) * u
+        g = torch.clamp(g, max=cfg.swiglu_limit)
+        u = torch.clamp(u, -cfg.swiglu_limit, cfg.swiglu_limit)
+        return g * torch.sigmoid(cfg.swiglu_alpha * g) * (u + 1)
+
+    def _moe(self, x, L):
+        """Routed experts (top-k softmax) + optional sigmoid-gated shared expert
+        (reference: MoeFfn, src/inference/layers/moe.rs)."""
+        cfg = self.cfg
+        k = cfg.n_experts_used
+        logits = x @ L.wr.T + (L.br if L.br is not None else 0)
+        top_v, top_i = torch.topk(logits, k, dim=-1)
+        if cfg.moe_softmax_after_topk:
+            w = torch.softmax(top_v, -1)
+        else:
+            w = torch.gather(torch.softmax(logits, -1), 1, top_i)
+        y = torch.zeros_like(x)
+        for e in top_i.unique().tolist():
+            sel = top_i == e
+            rows = sel.any(1).nonzero().flatten()
+            we = (w * sel).sum(1)[rows]
+            xs = x[rows]
+            g = xs @ L.eg[e].T + (L.ebg[e] if L.ebg is not None else 0)
+            u = xs @ L.eu[e].T + (L.ebu[e] if L.ebu is not None else 0)
+            o = self._act(g, u) @ L.ed[e].T + (L.ebd[e] if L.ebd is not None else 0)
+            y[rows] += we[:, None] * o
+        if L.sg is not None:
+            gate = torch.sigmoid(x @ L.sgi)[:, None]
+            y = y + gate * ((torch.nn.functional.silu(x @ L.sg.T) * (x @ L.su.T)) @ L.sd.T)
+        return y
 
     def forward(self, b: StepBatch, kv: PagedKVCache, ctx=None, h_in=None) -> torch.Tensor:
         cfg = self.cfg
@@ -334,8 +446,11 @@ class LlamaCPU:
                 o = o + L.bo
             h = h + o
             x = self._norm(h, L.ffn_norm)
-            gg, uu = x @ L.wg.T, x @ L.wu.T
-            h = h + (torch.nn.functional.silu(gg) * uu) @ L.wd.T
+            if L.moe:
+                h = h + self._moe(x, L)
+            else:
+                gg, uu = x @ L.wg.T, x @ L.wu.T
+                h = h + (torch.nn.functional.silu(gg) * uu) @ L.wd.T
         if not self.last:
             return h
         x = self._norm(h[b.sample_rows.long()], self.out_norm)

@@ -102,6 +102,9 @@ def _init_value(name: str, shape, rng: np.random.Generator, std: float) -> np.nd
         return rng.uniform(-1, 1, shape).astype(np.float32)
     if name.endswith("attn_sinks.weight"):
         return rng.standard_normal(shape).astype(np.float32)
+    if name.endswith("ffn_gate_inp.weight"):
+        # routers: peaked top-k (logit std ~ 5) like trained routers, not near-uniform
+        return (rng.standard_normal(shape, dtype=np.float32) * (5.0 / np.sqrt(shape[-1]))).astype(np.float32)
     return (rng.standard_normal(shape, dtype=np.float32) * std).astype(np.float32)
 
 

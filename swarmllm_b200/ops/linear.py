@@ -95,13 +95,16 @@ class QLinear:
         t = {"q4k": self.packed, "dense": self.w16, "simt": self.raw}[self.kind]
         return t.numel() * t.element_size()
 
-    def __call__(self, x: torch.Tensor, ws: GemmWorkspace):
+    def __call__(self, x: torch.Tensor, ws: GemmWorkspace, out: torch.Tensor | None = None):
+        """GEMM result of x [T, K] (fp16).  `out` (fp32 [T, rows]) gives the
+        CUDA-core path its own output instead of the workspace's dense buffer."""
         T = x.shape[0]
         if self.kind == "q4k":
             return C().qgemm_q4k_tc(self.packed, self.rows, self.K, x, ws.ws, ws.status, ws.num_sms)
         if self.kind == "dense":
             return C().dense_gemm_tc(self.w16, x, ws.ws, ws.status, ws.num_sms)
-        out = ws.dense(T * self.rows)[: T * self.rows].view(T, self.rows)
+        if out is None:
+            out = ws.dense(T * self.rows)[: T * self.rows].view(T, self.rows)
         return C().qmatmul_simt(self.raw, self.qtype, self.rows, self.K, x, out)
 
     def reference(self, x: torch.Tensor, ws: GemmWorkspace):

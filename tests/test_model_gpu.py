@@ -83,3 +83,55 @@ def test_engine_gpu_vs_cpu_greedy_tokens():
         prompts, SamplingParams(max_tokens=8))
     agree = np.mean([a == b for og, oc in zip(g, c) for a, b in zip(og.token_ids, oc.token_ids)])
     assert agree >= 0.9, (agree, [o.token_ids for o in g], [o.token_ids for o in c])
+
+
+def _moe_cfg(kind):
+    from swarmllm_b200.models.config import ModelConfig
+    if kind == "gpt-oss":
+        return ModelConfig(name="t-oss", arch="gpt-oss", n_layers=2, hidden=256, n_heads=8,
+                           n_kv_heads=2, head_dim=64, ffn=128, vocab=1024, rope_theta=150000.0,
+                           rope_neox=True, rope_scaling={"type": "yarn", "factor": 32.0,
+                                                         "original_max_position_embeddings": 4096,
+                                                         "beta_fast": 32.0, "beta_slow": 1.0},
+                           attn_bias=True, attn_sinks=True, sliding_window=16, swa_every=2,
+                           n_experts=8, n_experts_used=4, expert_ffn=128, swiglu_limit=7.0,
+                           weight_qtype="BF16", embed_qtype="BF16", output_qtype="BF16",
+                           expert_qtype="MXFP4")
+    return ModelConfig(name="t-moe", arch="qwen3moe", n_layers=2, hidden=512, n_heads=8,
+                       n_kv_heads=2, head_dim=64, ffn=256, vocab=1024, rms_eps=1e-6,
+                       qk_norm=True, rope_neox=True, n_experts=16, n_experts_used=4,
+                       expert_ffn=256, shared_expert_ffn=256, moe_softmax_after_topk=False,
+                       weight_qtype="Q4_K", embed_qtype="F16", output_qtype="Q4_K",
+                       expert_qtype="Q4_K")
+
+
+@pytest.mark.parametrize("kind", ["gpt-oss", "moe-shared"])
+def test_moe_model_matches_cpu_oracle(kind):
+    """MoE families: prefill + decode logits vs the fp32 oracle.  A routing
+    decision within rounding of a tie may flip between the two, so a few
+    positions may drift; the bulk must match closely."""
+    from swarmllm_b200.models.llama import LlamaCPU, LlamaGPU
+    from swarmllm_b200.models.weights import RandomSource
+    from swarmllm_b200.ops.attention import PagedKVCache
+    cfg = _moe_cfg(kind)
+    src = RandomSource(cfg, seed=11)
+    gpu = LlamaGPU(cfg, src, DEV)
+    cpu = LlamaCPU(cfg, src)
+    ctx = gpu.make_context(64, 40, 256)
+    kvg = PagedKVCache(cfg.n_layers, 8, cfg.n_kv_heads, cfg.head_dim, DEV)
+    kvc = PagedKVCache(cfg.n_layers, 8, cfg.n_kv_heads, cfg.head_dim, "cpu", dtype=torch.float32)
+    rng = np.random.default_rng(0)
+    toks = rng.integers(0, cfg.vocab, 43)
+    bt = np.tile(np.arange(8, dtype=np.int32), (64, 1))
+    pos = np.arange(40)
+    rows = list(range(40))
+    lg = gpu.forward(_batch(toks[:40], pos, pos, bt[:40], DEV, rows), kvg, ctx)
+    lc = cpu.forward(_batch(toks[:40], pos, pos, bt[:40], "cpu", rows), kvc)
+    ctx.moe.check()
+    cos = torch.nn.functional.cosine_similarity(lg.cpu().double(), lc.double(), dim=-1)
+    assert float(cos.median()) > 0.999 and float((cos > 0.995).float().mean()) >= 0.9, cos
+    for p in range(40, 43):
+        lg = gpu.forward(_batch([toks[p]], [p], [p], bt[:1], DEV, [0]), kvg, ctx)
+        lc = cpu.forward(_batch([toks[p]], [p], [p], bt[:1], "cpu", [0]), kvc)
+        cos = torch.nn.functional.cosine_similarity(lg.cpu().double(), lc.double(), dim=-1)
+        assert float(cos.min()) > 0.98, (p, cos)
