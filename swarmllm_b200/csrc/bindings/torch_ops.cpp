@@ -35,16 +35,18 @@ void epi_residual_rmsnorm(const GemmResult& g, Tensor residual, OptT bias, Tenso
 void epi_rope_kv(const GemmResult& g, OptT bias, Tensor positions, OptT slots, Tensor inv_freq,
                  int64_t n_q, int64_t n_kv, int64_t head_dim, int64_t rope_dim, bool neox,
                  double attn_factor, Tensor q_out, OptT k_cache, OptT v_cache, int64_t page_size,
-                 OptT q_norm_w, OptT k_norm_w, double norm_eps) {
+                 OptT q_norm_w, OptT k_norm_w, double norm_eps, OptT gate_out) {
   CHECK_DT(positions, at::kInt); CHECK_DT(q_out, at::kHalf); CHECK_DT(inv_freq, at::kFloat);
-  TORCH_CHECK(g.g.rows == (n_q + 2 * n_kv) * head_dim, "QKV rows mismatch");
+  TORCH_CHECK(g.g.rows == (n_q * (gate_out.has_value() ? 2 : 1) + 2 * n_kv) * head_dim,
+              "QKV rows mismatch");
   const at::cuda::CUDAGuard guard(q_out.device());
   launch_epi_rope_kv(g.g, ptr_or_null<float>(bias), positions.data_ptr<int32_t>(),
                      ptr_or_null<int32_t>(slots), inv_freq.data_ptr<float>(), (int)n_q, (int)n_kv,
                      (int)head_dim, (int)rope_dim, neox ? 1 : 0, (float)attn_factor,
                      reinterpret_cast<__half*>(q_out.data_ptr()), ptr_or_null<__half>(k_cache),
                      ptr_or_null<__half>(v_cache), (int)page_size, ptr_or_null<float>(q_norm_w),
-                     ptr_or_null<float>(k_norm_w), (float)norm_eps, cur_stream());
+                     ptr_or_null<float>(k_norm_w), (float)norm_eps, ptr_or_null<__half>(gate_out),
+                     cur_stream());
 }
 
 void epi_swiglu(const GemmResult& g, OptT bias, int64_t F, int64_t kind, bool interleaved,
@@ -264,7 +266,45 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_gather", &embed_gather);
   m.def("rmsnorm", &rmsnorm);
   m.def("epi_residual_rmsnorm", &epi_residual_rmsnorm);
-  m.def("epi_rope_kv", &epi_rope_kv);
+  m.def("epi_rope_kv", &epi_rope_kv, py::arg("g"), py::arg("bias"), py::arg("positions"),
+        py::arg("slots"), py::arg("inv_freq"), py::arg("n_q"), py::arg("n_kv"),
+        py::arg("head_dim"), py::arg("rope_dim"), py::arg("neox"), py::arg("attn_factor"),
+        py::arg("q_out"), py::arg("k_cache"), py::arg("v_cache"), py::arg("page_size"),
+        py::arg("q_norm_w"), py::arg("k_norm_w"), py::arg("norm_eps"),
+        py::arg("gate_out") = py::none());
+  m.def("mul_f16", [](Tensor x, Tensor y) {
+    CHECK_DT(x, at::kHalf); CHECK_DT(y, at::kHalf); CHECK_CONTIG(x); CHECK_CONTIG(y);
+    TORCH_CHECK(x.numel() == y.numel(), "size mismatch");
+    const at::cuda::CUDAGuard guard(x.device());
+    launch_mul_f16(reinterpret_cast<__half*>(x.data_ptr()),
+                   reinterpret_cast<const __half*>(y.data_ptr()), (size_t)x.numel(), cur_stream());
+  });
+  m.def("ssm_conv_silu", [](const GemmResult& g, Tensor w, Tensor state, Tensor seqs, int64_t S,
+                            Tensor out) {
+    CHECK_DT(w, at::kFloat); CHECK_DT(state, at::kFloat); CHECK_DT(seqs, at::kInt);
+    CHECK_DT(out, at::kFloat); CHECK_CONTIG(w); CHECK_CONTIG(out);
+    TORCH_CHECK(w.dim() == 2 && w.size(0) == g.g.rows, "conv weight [C, K]");
+    TORCH_CHECK(out.size(-1) == g.g.rows, "out width");
+    const at::cuda::CUDAGuard guard(out.device());
+    int rc = launch_ssm_conv_silu(g.g, w.data_ptr<float>(), (int)w.size(0), (int)w.size(1),
+                                  state.data_ptr<float>(), seqs.data_ptr(), (int)S,
+                                  out.data_ptr<float>(), cur_stream());
+    TORCH_CHECK(rc == 0, "ssm_conv_silu failed: rc=", rc);
+  });
+  m.def("delta_rule", [](Tensor qkv, int64_t nk, int64_t nv, int64_t D, const GemmResult& gba,
+                         Tensor dt_bias, Tensor A, const GemmResult& gz, Tensor norm_w, double eps,
+                         Tensor state, Tensor seqs, int64_t S, Tensor out) {
+    CHECK_DT(qkv, at::kFloat); CHECK_DT(state, at::kFloat); CHECK_DT(out, at::kHalf);
+    CHECK_DT(seqs, at::kInt); CHECK_CONTIG(qkv); CHECK_CONTIG(out);
+    TORCH_CHECK(qkv.size(-1) == (2 * nk + nv) * D, "qkv width");
+    const at::cuda::CUDAGuard guard(out.device());
+    int rc = launch_delta_rule(qkv.data_ptr<float>(), (int)qkv.size(-1), (int)nk, (int)nv, (int)D,
+                               gba.g, dt_bias.data_ptr<float>(), A.data_ptr<float>(), gz.g,
+                               norm_w.data_ptr<float>(), (float)eps, state.data_ptr<float>(),
+                               seqs.data_ptr(), (int)S, reinterpret_cast<__half*>(out.data_ptr()),
+                               cur_stream());
+    TORCH_CHECK(rc == 0, "delta_rule failed: rc=", rc);
+  });
   m.def("epi_swiglu", &epi_swiglu);
   m.def("epi_copy", &epi_copy);
   m.def("qmatmul_simt", &qmatmul_simt);

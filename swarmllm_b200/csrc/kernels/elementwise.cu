@@ -15,6 +15,7 @@
 //   epi_swiglu            silu(gate) * up, or gpt-oss clamped SwiGLU
 //                         (kernels/fused_decode.cu:47,68)
 //   epi_copy              GEMM out -> dense fp32 (logits)
+//   mul_f16               x *= y (gated attention: output * sigmoid(gate))
 #include "kernels.h"
 #include "gemm_out.cuh"
 #include "quant_blocks.cuh"
@@ -86,16 +87,32 @@ __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
                                    __half* __restrict__ q_out, __half* __restrict__ k_cache,
                                    __half* __restrict__ v_cache, int page_size,
                                    const float* __restrict__ q_norm_w,
-                                   const float* __restrict__ k_norm_w, float norm_eps) {
+                                   const float* __restrict__ k_norm_w, float norm_eps,
+                                   __half* __restrict__ gate_out) {
   extern __shared__ float sh[];  // (n_q + n_kv) * head_dim floats
   const int t = blockIdx.x;
   const int pos = positions[t];
   const int slot = slots ? slots[t] : -1;
   const int qk_rows = (n_q + n_kv) * head_dim;
   const int total = (n_q + 2 * n_kv) * head_dim;
+  const int q_rows = n_q * head_dim;
+  // Gated attention: each q head's GEMM rows are [q (head_dim) | gate (head_dim)];
+  // sigmoid(gate) goes to gate_out for the multiply after attention.
+  if (gate_out != nullptr) {
+    for (int i = threadIdx.x; i < q_rows; i += blockDim.x) {
+      const int h = i / head_dim, d = i - h * head_dim;
+      const float gv = g.get(t, h * 2 * head_dim + head_dim + d);
+      gate_out[(size_t)t * q_rows + i] = __float2half_rn(1.f / (1.f + __expf(-gv)));
+    }
+  }
   // Stage q and k (pre-RoPE) in shared memory; write v straight to the cache.
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
-    float v = g.get(t, i) + (bias ? bias[i] : 0.f);
+    int gr = i;  // GEMM row of logical row i
+    if (gate_out != nullptr) {
+      const int h = i / head_dim;
+      gr = (i < q_rows) ? i + h * head_dim : i + q_rows;
+    }
+    float v = g.get(t, gr) + (bias ? bias[i] : 0.f);
     if (i < qk_rows) {
       sh[i] = v;
     } else if (slot >= 0) {
@@ -186,6 +203,12 @@ __global__ void epi_copy_kernel(GemmOut g, const float* __restrict__ bias, float
     out[(size_t)t * out_stride + i] = g.get(t, i) + (bias ? bias[i] : 0.f);
 }
 
+__global__ void mul_f16_kernel(__half* __restrict__ x, const __half* __restrict__ y, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    x[i] = __hmul(x[i], y[i]);
+}
+
 __global__ void f32_to_f16_kernel(const float* __restrict__ x, __half* __restrict__ y,
                                    size_t n) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
@@ -229,7 +252,7 @@ void launch_epi_rope_kv(const GemmOut& g, const float* bias, const int32_t* posi
                         int head_dim, int rope_dim, int neox, float attn_factor,
                         __half* q_out, __half* k_cache, __half* v_cache, int page_size,
                         const float* q_norm_w, const float* k_norm_w, float norm_eps,
-                        cudaStream_t s) {
+                        __half* gate_out, cudaStream_t s) {
   if (g.T <= 0) return;
   size_t sm = (size_t)(n_q + n_kv) * head_dim * sizeof(float);
   if (sm > 48 * 1024)
@@ -237,7 +260,8 @@ void launch_epi_rope_kv(const GemmOut& g, const float* bias, const int32_t* posi
                          (int)sm);
   epi_rope_kv_kernel<<<g.T, 256, sm, s>>>(g, bias, positions, slots, inv_freq, n_q, n_kv,
                                           head_dim, rope_dim, neox, attn_factor, q_out, k_cache,
-                                          v_cache, page_size, q_norm_w, k_norm_w, norm_eps);
+                                          v_cache, page_size, q_norm_w, k_norm_w, norm_eps,
+                                          gate_out);
   SW_LAUNCH_CHECK();
 }
 
@@ -261,5 +285,12 @@ void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s) {
   if (n == 0) return;
   int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
   f32_to_f16_kernel<<<blocks, 256, 0, s>>>(x, y, n);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_mul_f16(__half* x, const __half* y, size_t n, cudaStream_t s) {
+  if (n == 0) return;
+  int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+  mul_f16_kernel<<<blocks, 256, 0, s>>>(x, y, n);
   SW_LAUNCH_CHECK();
 }

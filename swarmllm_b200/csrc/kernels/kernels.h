@@ -25,7 +25,7 @@ void launch_epi_rope_kv(const swarm::GemmOut& g, const float* bias, const int32_
                         const int32_t* slots, const float* inv_freq, int n_q, int n_kv,
                         int head_dim, int rope_dim, int neox, float attn_factor, __half* q_out,
                         __half* k_cache, __half* v_cache, int page_size, const float* q_norm_w,
-                        const float* k_norm_w, float norm_eps, cudaStream_t s);
+                        const float* k_norm_w, float norm_eps, __half* gate_out, cudaStream_t s);
 void launch_epi_swiglu(const swarm::GemmOut& g, const float* bias, int F, int kind,
                        int interleaved, float alpha, float limit, __half* out, cudaStream_t s);
 void launch_epi_copy(const swarm::GemmOut& g, const float* bias, float* out, int out_stride,
@@ -107,3 +107,14 @@ int launch_moe_combine(const float* rows, int row_stride, const float* wts, int 
                        const swarm::GemmOut* sh, const swarm::GemmOut* shg, float* residual,
                        int T, int H, const float* norm_w, __half* out, int out_stride, float eps,
                        cudaStream_t s);
+
+void launch_mul_f16(__half* x, const __half* y, size_t n, cudaStream_t s);
+
+// ---- gated DeltaNet (deltanet.cu) --------------------------------------------
+// seqs: int32 [S][4] = (row0, nrows, state slot, position of row0)
+int launch_ssm_conv_silu(const swarm::GemmOut& g, const float* w, int C, int K, float* state,
+                         const void* seqs, int S, float* out, cudaStream_t s);
+int launch_delta_rule(const float* qkv, int C, int nk, int nv, int D, const swarm::GemmOut& gba,
+                      const float* dt_bias, const float* A, const swarm::GemmOut& gz,
+                      const float* norm_w, float eps, float* state, const void* seqs, int S,
+                      __half* out, cudaStream_t s);

@@ -58,11 +58,19 @@ class LLMEngine:
         self.model = model
         N = native()
         ps = ecfg.page_size
+        lin = model.linear_state_spec() if hasattr(model, "linear_state_spec") else None
+        if lin is not None:
+            # recurrent state cannot be rebuilt from cached KV pages
+            ecfg.prefix_cache = False
+        n_kv_layers = getattr(model, "n_kv_layers", model.hi - model.lo)
         if self.device.type == "cuda":
             pages = ecfg.kv_pages or self._auto_pages()
             # one extra page: the trash page that graph padding rows write to
-            self.kv = PagedKVCache(model.hi - model.lo, pages + 1, cfg.n_kv_heads, cfg.head_dim,
+            self.kv = PagedKVCache(n_kv_layers, pages + 1, cfg.n_kv_heads, cfg.head_dim,
                                    self.device, ps)
+            if lin is not None:
+                self.kv.add_linear_state(lin[0], max(ecfg.max_running, max(ecfg.graph_sizes)) + 1,
+                                         *lin[1:])
             self.bm = N.BlockManager(pages, ps, ecfg.prefix_cache)
             self.runner = GpuRunner(model, self.kv, ecfg.max_step_tokens, ecfg.max_running,
                                     ecfg.max_model_len, ecfg.graph_sizes, ecfg.cuda_graphs,
@@ -71,11 +79,12 @@ class LLMEngine:
                 self.runner.capture_graphs()
         else:
             pages = ecfg.kv_pages or (ecfg.max_running * ((ecfg.max_model_len + ps - 1) // ps))
-            nl = model.hi - model.lo
-            self.kv = PagedKVCache(nl, pages, cfg.n_kv_heads, cfg.head_dim, "cpu", ps,
+            self.kv = PagedKVCache(n_kv_layers, pages, cfg.n_kv_heads, cfg.head_dim, "cpu", ps,
                                    dtype=torch.float32)
+            if lin is not None:
+                self.kv.add_linear_state(lin[0], ecfg.max_running + 1, *lin[1:])
             self.bm = N.BlockManager(pages, ps, ecfg.prefix_cache)
-            self.runner = CpuRunner(model, self.kv, ecfg.max_model_len)
+            self.runner = CpuRunner(model, self.kv, ecfg.max_model_len, ecfg.max_running)
         self.sched = N.Scheduler(self.bm, ecfg.max_step_tokens, ecfg.max_running, ecfg.prefill_chunk)
         self.params: dict[int, SamplingParams] = {}
         self.traces: dict[int, RequestTrace] = {}
@@ -108,7 +117,9 @@ class LLMEngine:
 
     def _auto_pages(self) -> int:
         free, _ = torch.cuda.mem_get_info(self.device)
-        per_page = PagedKVCache.bytes_per_page(self.model.hi - self.model.lo, self.cfg.n_kv_heads,
+        per_page = PagedKVCache.bytes_per_page(getattr(self.model, "n_kv_layers",
+                                                       self.model.hi - self.model.lo),
+                                               self.cfg.n_kv_heads,
                                                self.cfg.head_dim, self.ecfg.page_size)
         # leave room for activations / workspaces
         budget = free * self.ecfg.kv_fraction - 4 * (1 << 30)
@@ -130,6 +141,12 @@ class LLMEngine:
 
     def abort(self, rid: int):
         self.sched.abort(rid)
+        self._free_state(rid)
+
+    def _free_state(self, rid: int):
+        slots = getattr(self.runner, "slots", None)
+        if slots is not None:
+            slots.release(rid)
 
     def has_work(self) -> bool:
         return self.sched.has_work()
@@ -183,6 +200,7 @@ class LLMEngine:
 
     def release(self, rid: int):
         self.sched.release(rid)
+        self._free_state(rid)
         self.params.pop(rid, None)
         self.prompt_len.pop(rid, None)
 

@@ -39,6 +39,38 @@ def plan_arrays(plan, block_manager, max_pages: int):
     return tokens, positions, slots, bt_rows, seq_lens, sample_rows
 
 
+class StateSlots:
+    """Recurrent-state slots of the linear-attention layers, one per live
+    sequence; the last slot takes graph padding rows."""
+
+    def __init__(self, n: int):
+        self.free = list(range(n - 1, -1, -1))
+        self.of: dict[int, int] = {}
+        self.trash = n
+
+    def get(self, sid: int) -> int:
+        s = self.of.get(sid)
+        if s is None:
+            if not self.free:
+                raise RuntimeError("no free linear-attention state slot")
+            s = self.of[sid] = self.free.pop()
+        return s
+
+    def release(self, sid: int):
+        s = self.of.pop(sid, None)
+        if s is not None:
+            self.free.append(s)
+
+
+def ssm_table(plan, positions, slots: StateSlots) -> np.ndarray:
+    """int32 [S, 4] (row0, nrows, state slot, position of row0) per sequence."""
+    out = np.zeros((len(plan.seq_ids), 4), np.int32)
+    for b, sid in enumerate(plan.seq_ids):
+        r0, n = int(plan.seq_start[b]), int(plan.seq_ntok[b])
+        out[b] = (r0, n, slots.get(int(sid)), int(positions[r0]) if n else 0)
+    return out
+
+
 def attention_groups(plan, n_rep: int):
     """Row groups for the tensor-core attention kernel: runs of at most
     128 // n_rep consecutive positions of one sequence (None if every
@@ -83,6 +115,12 @@ class GpuRunner:
         self.graph_sizes = sorted(s for s in graph_sizes if s <= min(max_tokens, max_seqs))
         self.use_graphs = use_graphs
         self.graphs: dict[int, tuple] = {}
+        self.slots = None
+        if getattr(model, "n_lin_layers", 0):
+            ms = max(max_seqs, max(graph_sizes))
+            self.slots = StateSlots(max_seqs)
+            self.d_ssm = torch.zeros(ms, 4, dtype=torch.int32, device=dev)
+            self.h_ssm = torch.zeros(ms, 4, dtype=torch.int32).pin_memory()
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.launches_per_step = None
@@ -117,9 +155,25 @@ class GpuRunner:
         self.h2d_bytes = 4 * 4 * M + 4 * M * self.max_pages + 8 * Sm
         return M, Sm
 
-    def _batch(self, M: int, S: int) -> StepBatch:
-        return StepBatch(self.d_tokens[:M], self.d_pos[:M], self.d_slots[:M], self.d_bt[:M],
-                         self.d_lens[:M], self.d_samp[:S], self.max_model_len)
+    def _upload_ssm(self, table: np.ndarray, pad_to: int = 0) -> int:
+        n = len(table)
+        m = max(n, pad_to)
+        self.h_ssm[:n] = torch.from_numpy(table)
+        if m > n:  # padding sequences: no rows
+            self.h_ssm[n:m, 0] = 0
+            self.h_ssm[n:m, 1] = 0
+            self.h_ssm[n:m, 2] = self.slots.trash
+            self.h_ssm[n:m, 3] = 0
+        self.d_ssm[:m].copy_(self.h_ssm[:m], non_blocking=True)
+        self.h2d_bytes += 16 * m
+        return m
+
+    def _batch(self, M: int, S: int, n_seqs: int = 0) -> StepBatch:
+        b = StepBatch(self.d_tokens[:M], self.d_pos[:M], self.d_slots[:M], self.d_bt[:M],
+                      self.d_lens[:M], self.d_samp[:S], self.max_model_len)
+        if self.slots is not None:
+            b.ssm_seqs = self.d_ssm[:n_seqs]
+        return b
 
     # ------------------------------------------------------------------ graphs
     def capture_graphs(self):
@@ -129,7 +183,7 @@ class GpuRunner:
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             for B in self.graph_sizes:
-                b = self._batch(B, B)
+                b = self._batch(B, B, B)
                 self._init_dummy(B)
                 for _ in range(2):  # warm up (sets kernel attributes, tensor maps)
                     self.model.forward(b, self.kv, self.ctx)
@@ -148,6 +202,11 @@ class GpuRunner:
         self.d_lens[:B] = 1
         self.d_bt[:B] = self.trash_page
         self.d_samp[:B] = torch.arange(B, device=self.device)
+        if self.slots is not None:
+            self.d_ssm[:B, 0] = torch.arange(B, device=self.device, dtype=torch.int32)
+            self.d_ssm[:B, 1] = 0
+            self.d_ssm[:B, 2] = self.slots.trash
+            self.d_ssm[:B, 3] = 0
 
     # ------------------------------------------------------------------ step
     def run(self, plan, block_manager, params: list[SamplingParams]) -> np.ndarray:
@@ -159,14 +218,18 @@ class GpuRunner:
         decode_only = plan.n_prefill_tokens == 0 and N == S
         greedy = all(p.greedy for p in params)
         B = next((b for b in self.graph_sizes if b >= N), None) if decode_only else None
+        table = ssm_table(plan, positions, self.slots) if self.slots is not None else None
         if B is not None and B in self.graphs and greedy:
             self._upload(tokens, positions, slots, bt_rows, seq_lens, sample_rows, pad_to=B)
+            if table is not None:
+                self._upload_ssm(table, pad_to=B)
             g, logits, out = self.graphs[B]
             g.replay()
             res = out[:S]
         else:
             M, _ = self._upload(tokens, positions, slots, bt_rows, seq_lens, sample_rows)
-            b = self._batch(M, S)
+            ns = self._upload_ssm(table) if table is not None else 0
+            b = self._batch(M, S, ns)
             cfg = self.model.cfg
             grp = attention_groups(plan, cfg.n_heads // cfg.n_kv_heads)
             if grp is not None:
@@ -181,10 +244,11 @@ class GpuRunner:
 
 
 class CpuRunner:
-    def __init__(self, model, kv: PagedKVCache, max_model_len: int):
+    def __init__(self, model, kv: PagedKVCache, max_model_len: int, max_seqs: int = 64):
         self.model, self.kv = model, kv
         self.max_model_len = max_model_len
         self.max_pages = (max_model_len + kv.page_size - 1) // kv.page_size
+        self.slots = StateSlots(max_seqs) if getattr(model, "n_lin_layers", 0) else None
 
     def forward_plan(self, plan, block_manager, h_in=None):
         tokens, positions, slots, bt_rows, seq_lens, sample_rows = plan_arrays(
@@ -193,6 +257,8 @@ class CpuRunner:
                       torch.from_numpy(np.asarray(positions, np.int32)),
                       torch.from_numpy(np.asarray(slots, np.int32)), torch.from_numpy(bt_rows),
                       torch.from_numpy(seq_lens), torch.from_numpy(sample_rows), self.max_model_len)
+        if self.slots is not None:
+            b.ssm_seqs = torch.from_numpy(ssm_table(plan, positions, self.slots))
         return self.model.forward(b, self.kv, None, h_in), positions, sample_rows
 
     def run(self, plan, block_manager, params: list[SamplingParams]) -> np.ndarray:

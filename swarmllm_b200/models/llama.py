@@ -46,6 +46,7 @@ class StepBatch:
     tree_mask: torch.Tensor | None = None   # uint64 [N] (as int64)
     tree_start: torch.Tensor | None = None  # int32 [N]
     groups: tuple | None = None             # (row0 int32[G], npos int32[G], positions/group)
+    ssm_seqs: torch.Tensor | None = None    # int32 [S, 4] (row0, nrows, state slot, pos0): linear attention
 
 
 def _f32(t: torch.Tensor, qt: int, shape) -> torch.Tensor:
@@ -82,27 +83,37 @@ class LlamaGPU:
             t, qt, shape = get("token_embd.weight")
             self.embd, self.embd_type = t, qt
         self.layers = []
+        n_attn = n_lin = 0
         for i in range(lo, hi):
             b = f"blk.{i}."
             L = _GpuLayer()
             L.attn_norm = small(b + "attn_norm.weight")
             L.ffn_norm = small(b + "ffn_norm.weight")
-            parts = [get(b + n) for n in ("attn_q.weight", "attn_k.weight", "attn_v.weight")]
-            qt = parts[0][1]
-            assert all(p[1] == qt for p in parts), "q/k/v must share a quant type"
-            rows = sum(p[2][0] for p in parts)
-            L.wqkv = QLinear(torch.cat([p[0] for p in parts]), qt, rows, H, dev)
-            L.qkv_bias = None
-            if cfg.attn_bias:
-                L.qkv_bias = torch.cat([small(b + n) for n in
-                                        ("attn_q.bias", "attn_k.bias", "attn_v.bias")])
-            t, qt, shape = get(b + "attn_output.weight")
-            L.wo = QLinear(t, qt, shape[0], shape[1], dev)
-            L.o_bias = small(b + "attn_output.bias") if cfg.attn_bias else None
-            L.q_norm = small(b + "attn_q_norm.weight") if cfg.qk_norm else None
-            L.k_norm = small(b + "attn_k_norm.weight") if cfg.qk_norm else None
-            L.sinks = small(b + "attn_sinks.weight") if cfg.attn_sinks else None
-            L.window = cfg.sliding_window if cfg.is_swa(i) else 0
+            L.linear = cfg.is_linear_attn(i)
+            if L.linear:
+                L.lin_idx = n_lin
+                n_lin += 1
+                self._load_deltanet(L, b, get, small)
+            else:
+                L.kv_idx = n_attn
+                n_attn += 1
+                parts = [get(b + n) for n in ("attn_q.weight", "attn_k.weight", "attn_v.weight")]
+                qt = parts[0][1]
+                assert all(p[1] == qt for p in parts), "q/k/v must share a quant type"
+                rows = sum(p[2][0] for p in parts)
+                L.wqkv = QLinear(torch.cat([p[0] for p in parts]), qt, rows, H, dev)
+                L.qkv_bias = None
+                if cfg.attn_bias:
+                    L.qkv_bias = torch.cat([small(b + n) for n in
+                                            ("attn_q.bias", "attn_k.bias", "attn_v.bias")])
+                t, qt, shape = get(b + "attn_output.weight")
+                L.wo = QLinear(t, qt, shape[0], shape[1], dev)
+                L.o_bias = small(b + "attn_output.bias") if cfg.attn_bias else None
+                L.q_norm = small(b + "attn_q_norm.weight") if cfg.qk_norm else None
+                L.k_norm = small(b + "attn_k_norm.weight") if cfg.qk_norm else None
+                L.sinks = small(b + "attn_sinks.weight") if cfg.attn_sinks else None
+                L.window = cfg.sliding_window if cfg.is_swa(i) else 0
+                L.gated = cfg.attn_output_gate
             L.experts = None
             if cfg.n_experts:
                 self._load_moe(L, b, get, small)
@@ -112,6 +123,7 @@ class LlamaGPU:
                 t, qt, shape = get(b + "ffn_down.weight")
                 L.wdown = QLinear(t, qt, shape[0], shape[1], dev)
             self.layers.append(L)
+        self.n_kv_layers, self.n_lin_layers = n_attn, n_lin
         self.next_norm = None
         if self.last:
             self.out_norm = small("output_norm.weight")
@@ -121,6 +133,33 @@ class LlamaGPU:
         inv, self.attn_factor = rope_inv_freq(cfg)
         self.inv_freq = torch.from_numpy(inv).to(dev)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    def _load_deltanet(self, L, b, get, small):
+        """Gated DeltaNet layer: in-projection (q|k|v), z gate, beta/decay
+        projection, conv1d, decay parameters, gated norm, out-projection."""
+        cfg, dev, H = self.cfg, self.device, self.cfg.hidden
+        nv, dh = cfg.ssm_v_heads, cfg.ssm_head_dim
+        t, qt, shape = get(b + "attn_qkv.weight")
+        L.w_in = QLinear(t, qt, shape[0], H, dev)
+        t, qt, shape = get(b + "attn_gate.weight")
+        L.w_z = QLinear(t, qt, shape[0], H, dev)
+        t, qt, shape = get(b + "ssm_ba.weight")
+        L.w_ba = QLinear(t, qt, 2 * nv, H, dev)
+        L.conv_w = small(b + "ssm_conv1d.weight").contiguous()
+        L.dt_bias = small(b + "ssm_dt.bias")
+        L.A = small(b + "ssm_a")
+        L.ssm_norm = small(b + "ssm_norm.weight")
+        t, qt, shape = get(b + "ssm_out.weight")
+        L.w_out = QLinear(t, qt, H, nv * dh, dev)
+
+    def linear_state_spec(self):
+        """(n_layers, nv, dk, dv, conv_channels, conv_k) of this stage's
+        linear-attention layers, or None."""
+        if not self.n_lin_layers:
+            return None
+        c = self.cfg
+        return (self.n_lin_layers, c.ssm_v_heads, c.ssm_head_dim, c.ssm_head_dim,
+                (2 * c.ssm_k_heads + c.ssm_v_heads) * c.ssm_head_dim, c.ssm_conv_kernel)
 
     def _load_moe(self, L, b, get, small):
         """Routed experts (+ router, + shared expert) of one layer."""
@@ -155,7 +194,10 @@ class LlamaGPU:
 
     def _linears(self):
         for L in self.layers:
-            yield from (L.wqkv, L.wo)
+            if L.linear:
+                yield from (L.w_in, L.w_z, L.w_out)
+            else:
+                yield from (L.wqkv, L.wo)
             if L.experts is None:
                 yield from (L.wgu, L.wdown)
             elif L.sh_gu is not None:
@@ -174,9 +216,23 @@ class LlamaGPU:
         c = self.cfg
         r = max(c.q_dim * (2 if c.attn_output_gate else 1) + 2 * c.kv_dim, 2 * c.ffn, c.hidden,
                 2 * c.shared_expert_ffn)
+        if self.n_lin_layers:
+            r = max(r, (2 * c.ssm_k_heads + c.ssm_v_heads) * c.ssm_head_dim)
         if self.last:
             r = max(r, c.vocab)
         return r
+
+    def _deltanet(self, L, b, kv, ctx, x, N):
+        """Gated DeltaNet token mixing of one layer -> ctx.ssm_out (fp16)."""
+        cfg = self.cfg
+        nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
+        S = b.ssm_seqs.shape[0]
+        g = L.w_in(x, ctx.gemm)
+        C().ssm_conv_silu(g, L.conv_w, kv.conv_state(L.lin_idx), b.ssm_seqs, S, ctx.ssm_qkv[:N])
+        gba = L.w_ba(x, ctx.gemm, out=ctx.ssm_ba[:N])
+        gz = L.w_z(x, ctx.gemm)  # the conv consumed the in-projection's workspace already
+        C().delta_rule(ctx.ssm_qkv[:N], nk, nv, dh, gba, L.dt_bias, L.A, gz, L.ssm_norm,
+                       cfg.rms_eps, kv.ssm_state(L.lin_idx), b.ssm_seqs, S, ctx.ssm_out[:N])
 
     def make_context(self, max_tokens: int, max_samples: int, max_len: int):
         return GpuForwardContext(self, max_tokens, max_samples, max_len)
@@ -197,17 +253,25 @@ class LlamaGPU:
         ao = ctx.attn_out[:N]
         act = ctx.act[:N]
         for j, L in enumerate(self.layers):
-            li = self.kv_off + j
-            g = L.wqkv(x, ctx.gemm)
-            C().epi_rope_kv(g, L.qkv_bias, b.positions, b.slots, self.inv_freq, nq, nkv, d,
-                            cfg.rot_dim, cfg.rope_neox, self.attn_factor, q, kv.k(li), kv.v(li),
-                            kv.page_size, L.q_norm, L.k_norm, cfg.rms_eps)
-            paged_attention(q, kv.k(li), kv.v(li), b.block_table, b.seq_lens, ctx.attn,
-                            ao.view(N, nq, d), b.max_len, self.scale, L.window, L.sinks,
-                            tree_mask=b.tree_mask, tree_start=b.tree_start,
-                            num_sms=ctx.gemm.num_sms, groups=b.groups)
-            g = L.wo(ao, ctx.gemm)
-            C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
+            if L.linear:
+                self._deltanet(L, b, kv, ctx, x, N)
+                g = L.w_out(ctx.ssm_out[:N], ctx.gemm)
+                C().epi_residual_rmsnorm(g, h, None, L.ffn_norm, x, cfg.rms_eps)
+            else:
+                li = self.kv_off + L.kv_idx
+                g = L.wqkv(x, ctx.gemm)
+                gate = ctx.gate[:N] if L.gated else None
+                C().epi_rope_kv(g, L.qkv_bias, b.positions, b.slots, self.inv_freq, nq, nkv, d,
+                                cfg.rot_dim, cfg.rope_neox, self.attn_factor, q, kv.k(li),
+                                kv.v(li), kv.page_size, L.q_norm, L.k_norm, cfg.rms_eps, gate)
+                paged_attention(q, kv.k(li), kv.v(li), b.block_table, b.seq_lens, ctx.attn,
+                                ao.view(N, nq, d), b.max_len, self.scale, L.window, L.sinks,
+                                tree_mask=b.tree_mask, tree_start=b.tree_start,
+                                num_sms=ctx.gemm.num_sms, groups=b.groups)
+                if gate is not None:
+                    C().mul_f16(ao, gate)
+                g = L.wo(ao, ctx.gemm)
+                C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
             if j + 1 < len(self.layers):
                 nxt_w, nxt_out = self.layers[j + 1].attn_norm, x
             elif self.last:
@@ -259,6 +323,14 @@ class GpuForwardContext:
         self.xs = torch.zeros(max_samples, H, dtype=torch.float16, device=dev)
         self.logits = torch.zeros(max_samples, cfg.vocab, dtype=torch.float32, device=dev)
         self.dummy_norm = torch.ones(H, dtype=torch.float32, device=dev)
+        if cfg.attn_output_gate:
+            self.gate = torch.zeros(max_tokens, cfg.q_dim, dtype=torch.float16, device=dev)
+        if model.n_lin_layers:
+            nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
+            self.ssm_qkv = torch.zeros(max_tokens, (2 * nk + nv) * dh, dtype=torch.float32,
+                                       device=dev)
+            self.ssm_ba = torch.zeros(max_tokens, 2 * nv, dtype=torch.float32, device=dev)
+            self.ssm_out = torch.zeros(max_tokens, nv * dh, dtype=torch.float16, device=dev)
         self.moe = None
         if cfg.n_experts:
             ex = next(L.experts for L in model.layers if L.experts is not None)
@@ -297,10 +369,23 @@ class LlamaCPU:
         if self.first:
             self.embd = dq("token_embd.weight")
         self.layers = []
+        n_attn = n_lin = 0
         for i in range(lo, hi):
             b = f"blk.{i}."
             L = _GpuLayer()
             L.attn_norm, L.ffn_norm = dq(b + "attn_norm.weight"), dq(b + "ffn_norm.weight")
+            L.linear = cfg.is_linear_attn(i)
+            if L.linear:
+                L.lin_idx = n_lin
+                n_lin += 1
+                L.w_in, L.w_z, L.w_ba = dq(b + "attn_qkv.weight"), dq(b + "attn_gate.weight"), dq(b + "ssm_ba.weight")
+                L.conv_w, L.dt_bias, L.A = dq(b + "ssm_conv1d.weight"), dq(b + "ssm_dt.bias"), dq(b + "ssm_a")
+                L.ssm_norm, L.w_out = dq(b + "ssm_norm.weight"), dq(b + "ssm_out.weight")
+                self._load_ffn_cpu(L, b, dq)
+                self.layers.append(L)
+                continue
+            L.kv_idx = n_attn
+            n_attn += 1
             L.wq, L.wk, L.wv = dq(b + "attn_q.weight"), dq(b + "attn_k.weight"), dq(b + "attn_v.weight")
             L.wo = dq(b + "attn_output.weight")
             L.bq = dq(b + "attn_q.bias") if cfg.attn_bias else None
@@ -311,30 +396,37 @@ class LlamaCPU:
             L.k_norm = dq(b + "attn_k_norm.weight") if cfg.qk_norm else None
             L.sinks = dq(b + "attn_sinks.weight") if cfg.attn_sinks else None
             L.window = cfg.sliding_window if cfg.is_swa(i) else 0
-            L.moe = bool(cfg.n_experts)
-            if L.moe:
-                gpt = cfg.arch == "gpt-oss"
-                L.wr = dq(b + "ffn_gate_inp.weight")
-                L.br = dq(b + "ffn_gate_inp.bias") if gpt else None
-                L.eg, L.eu, L.ed = (dq(b + n) for n in ("ffn_gate_exps.weight", "ffn_up_exps.weight",
-                                                         "ffn_down_exps.weight"))
-                L.ebg = dq(b + "ffn_gate_exps.bias") if gpt else None
-                L.ebu = dq(b + "ffn_up_exps.bias") if gpt else None
-                L.ebd = dq(b + "ffn_down_exps.bias") if gpt else None
-                L.sg = None
-                if cfg.shared_expert_ffn:
-                    L.sg, L.su, L.sd = (dq(b + n) for n in ("ffn_gate_shexp.weight", "ffn_up_shexp.weight",
-                                                             "ffn_down_shexp.weight"))
-                    L.sgi = dq(b + "ffn_gate_inp_shexp.weight")
-            else:
-                L.wg, L.wu, L.wd = dq(b + "ffn_gate.weight"), dq(b + "ffn_up.weight"), dq(b + "ffn_down.weight")
+            self._load_ffn_cpu(L, b, dq)
             self.layers.append(L)
+        self.n_kv_layers, self.n_lin_layers = n_attn, n_lin
         if self.last:
             self.out_norm = dq("output_norm.weight")
             self.head = dq("token_embd.weight" if cfg.tie_embeddings else "output.weight")
         inv, self.attn_factor = rope_inv_freq(cfg)
         self.inv_freq = torch.from_numpy(inv)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    linear_state_spec = LlamaGPU.linear_state_spec
+
+    def _load_ffn_cpu(self, L, b, dq):
+        cfg = self.cfg
+        L.moe = bool(cfg.n_experts)
+        if L.moe:
+            gpt = cfg.arch == "gpt-oss"
+            L.wr = dq(b + "ffn_gate_inp.weight")
+            L.br = dq(b + "ffn_gate_inp.bias") if gpt else None
+            L.eg, L.eu, L.ed = (dq(b + n) for n in ("ffn_gate_exps.weight", "ffn_up_exps.weight",
+                                                     "ffn_down_exps.weight"))
+            L.ebg = dq(b + "ffn_gate_exps.bias") if gpt else None
+            L.ebu = dq(b + "ffn_up_exps.bias") if gpt else None
+            L.ebd = dq(b + "ffn_down_exps.bias") if gpt else None
+            L.sg = None
+            if cfg.shared_expert_ffn:
+                L.sg, L.su, L.sd = (dq(b + n) for n in ("ffn_gate_shexp.weight", "ffn_up_shexp.weight",
+                                                         "ffn_down_shexp.weight"))
+                L.sgi = dq(b + "ffn_gate_inp_shexp.weight")
+        else:
+            L.wg, L.wu, L.wd = dq(b + "ffn_gate.weight"), dq(b + "ffn_up.weight"), dq(b + "ffn_down.weight")
 
     def _norm(self, x, w):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.rms_eps) * w
@@ -364,6 +456,54 @@ class LlamaCPU:
         g = torch.clamp(g, max=cfg.swiglu_limit)
         u = torch.clamp(u, -cfg.swiglu_limit, cfg.swiglu_limit)
         return g * torch.sigmoid(cfg.swiglu_alpha * g) * (u + 1)
+
+    def _ffn(self, L, x):
+        if L.moe:
+            return self._moe(x, L)
+        return (torch.nn.functional.silu(x @ L.wg.T) * (x @ L.wu.T)) @ L.wd.T
+
+    def _deltanet(self, L, x, b, kv):
+        """Gated DeltaNet (sequential recurrence, the definition the GPU
+        kernels implement): conv1d + SiLU, L2-normalised q/k, decay and beta
+        gates, delta-rule state update, gated RMSNorm, out-projection."""
+        cfg = self.cfg
+        nk, nv, D = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
+        K = cfg.ssm_conv_kernel
+        rep = nv // nk
+        N = x.shape[0]
+        qkv, z, ba = x @ L.w_in.T, x @ L.w_z.T, x @ L.w_ba.T
+        conv_st, ssm_st = kv.conv_state(L.lin_idx), kv.ssm_state(L.lin_idx)
+        out = torch.zeros(N, nv * D, dtype=x.dtype)
+        for r0, n, slot, p0 in b.ssm_seqs.tolist():
+            if n <= 0:
+                continue
+            win = torch.zeros(K - 1, qkv.shape[1], dtype=x.dtype) if p0 == 0 else conv_st[slot].to(x.dtype)
+            xs = torch.cat([win, qkv[r0:r0 + n]], 0)
+            act = sum(L.conv_w[:, i] * xs[i:i + n] for i in range(K))
+            act = torch.nn.functional.silu(act)
+            conv_st[slot] = xs[-(K - 1):].to(conv_st.dtype)
+            S = torch.zeros(nv, D, D, dtype=x.dtype) if p0 == 0 else ssm_st[slot].to(x.dtype)
+            for t in range(n):
+                a = act[t]
+                q = a[:nk * D].view(nk, D)
+                k = a[nk * D:2 * nk * D].view(nk, D)
+                v = a[2 * nk * D:].view(nv, D)
+                q = q * torch.rsqrt(q.pow(2).sum(-1, keepdim=True) + 1e-6) / math.sqrt(D)
+                k = k * torch.rsqrt(k.pow(2).sum(-1, keepdim=True) + 1e-6)
+                q, k = q.repeat_interleave(rep, 0), k.repeat_interleave(rep, 0)
+                r = r0 + t
+                beta = torch.sigmoid(ba[r, :nv])
+                g = L.A * torch.nn.functional.softplus(ba[r, nv:] + L.dt_bias)
+                S = S * torch.exp(g)[:, None, None]
+                kvm = torch.einsum("hij,hi->hj", S, k)
+                dl = (v - kvm) * beta[:, None]
+                S = S + k[:, :, None] * dl[:, None, :]
+                o = torch.einsum("hij,hi->hj", S, q)
+                o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + cfg.rms_eps) * L.ssm_norm
+                o = o * torch.nn.functional.silu(z[r].view(nv, D))
+                out[r] = o.flatten()
+            ssm_st[slot] = S.to(ssm_st.dtype)
+        return out @ L.w_out.T
 
     def _moe(self, x, L):
         """Routed experts (top-k softmax) + optional sigmoid-gated shared expert
@@ -401,14 +541,23 @@ class LlamaCPU:
         slots = b.slots.long()
         pages, offs = slots // ps, slots % ps
         for j, L in enumerate(self.layers):
-            li = self.kv_off + j
             x = self._norm(h, L.attn_norm)
+            if L.linear:
+                h = h + self._deltanet(L, x, b, kv)
+                x = self._norm(h, L.ffn_norm)
+                h = h + self._ffn(L, x)
+                continue
+            li = self.kv_off + L.kv_idx
             q = x @ L.wq.T
             k = x @ L.wk.T
             v = x @ L.wv.T
+            gate = None
+            if cfg.attn_output_gate:
+                qg = q.view(N, nq, 2 * d)
+                q, gate = qg[..., :d], torch.sigmoid(qg[..., d:]).reshape(N, nq * d)
             if L.bq is not None:
                 q, k, v = q + L.bq, k + L.bk, v + L.bv
-            q, k, v = q.view(N, nq, d), k.view(N, nkv, d), v.view(N, nkv, d)
+            q, k, v = q.reshape(N, nq, d), k.view(N, nkv, d), v.view(N, nkv, d)
             if L.q_norm is not None:
                 q, k = self._norm(q, L.q_norm), self._norm(k, L.k_norm)
             q, k = self._rope(q, b.positions), self._rope(k, b.positions)
@@ -441,16 +590,15 @@ class LlamaCPU:
                 if L.sinks is not None:
                     p = p[:, :-1]
                 att[t] = torch.einsum("hn,nhd->hd", p, vv)
-            o = att.view(N, nq * d) @ L.wo.T
+            a = att.view(N, nq * d)
+            if gate is not None:
+                a = a * gate
+            o = a @ L.wo.T
             if L.bo is not None:
                 o = o + L.bo
             h = h + o
             x = self._norm(h, L.ffn_norm)
-            if L.moe:
-                h = h + self._moe(x, L)
-            else:
-                gg, uu = x @ L.wg.T, x @ L.wu.T
-                h = h + (torch.nn.functional.silu(gg) * uu) @ L.wd.T
+            h = h + self._ffn(L, x)
         if not self.last:
             return h
         x = self._norm(h[b.sample_rows.long()], self.out_norm)

@@ -19,6 +19,23 @@ class PagedKVCache:
         self.data = torch.zeros(n_layers, 2, num_pages, n_kv, page_size, head_dim, dtype=dtype,
                                 device=device)
 
+        self.ssm = self.conv = None
+
+    def add_linear_state(self, n_layers: int, slots: int, nv: int, dk: int, dv: int,
+                         conv_channels: int, conv_k: int):
+        """Recurrent state of the linear-attention (gated DeltaNet) layers:
+        per layer and sequence slot, S [nv][dk][dv] and the conv window
+        [conv_k - 1][channels], fp32."""
+        dev, dt = self.data.device, torch.float32
+        self.ssm = torch.zeros(n_layers, slots, nv, dk, dv, dtype=dt, device=dev)
+        self.conv = torch.zeros(n_layers, slots, conv_k - 1, conv_channels, dtype=dt, device=dev)
+
+    def ssm_state(self, layer: int) -> torch.Tensor:
+        return self.ssm[layer]
+
+    def conv_state(self, layer: int) -> torch.Tensor:
+        return self.conv[layer]
+
     def k(self, layer: int) -> torch.Tensor:
         return self.data[layer, 0]
 
