@@ -45,6 +45,7 @@ def parse():
     p.add_argument("--prompt", type=int, default=2048)
     p.add_argument("--gen", type=int, default=512)
     p.add_argument("--ttft-reps", type=int, default=3)
+    p.add_argument("--chunk", type=int, default=0, help="prefill chunk (0: whole prompt)")
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the headline)")
     return p.parse_args()
 
@@ -123,8 +124,9 @@ def single_gpu(args):
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
     B, P, G = args.batch, args.prompt, args.gen
-    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=B, max_step_tokens=P,
-                        prefill_chunk=P, graph_sizes=(1, B))
+    chunk = args.chunk or P
+    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=B, max_step_tokens=chunk,
+                        prefill_chunk=chunk, graph_sizes=(1, B))
     t0 = time.time()
     eng = LLMEngine.from_config(cfg, dev, ecfg, seed=1234)
     t_init = time.time() - t0
@@ -185,17 +187,22 @@ def single_gpu(args):
     ms32, e2e32, clocks, h2d, d2h = decode_rate(B, args.steps, args.warmup)
     ms1, e2e1, _, _, _ = decode_rate(1, args.steps, args.warmup)
     value = B * args.steps / (ms32 / 1e3)
-    launches = kernel_launches_per_step(eng.model) * args.steps
+    launches = eng.model.decode_launches() * args.steps
+    headline = cfg.name == "llama-3.3-70b"
+    wq = cfg.expert_qtype if cfg.n_experts else cfg.weight_qtype
     line = {
-        "metric": f"decode tok/s at batch {B} (aggregate), Llama-3.3-70B Q4_K",
+        "metric": (f"decode tok/s at batch {B} (aggregate), Llama-3.3-70B Q4_K" if headline else
+                   f"decode tok/s at batch {B} (aggregate), {cfg.name}"),
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms32 / args.steps, 4),
         "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": round(value / BASELINE_70B_TOKS, 2), "dtype": "fp16 activations, fp32 accumulate, Q4_K weights",
-        "data": "synthetic uniform-random token ids; random-init Q4_K weights (llama-3.3-70b architecture)",
+        "vs_baseline": round(value / BASELINE_70B_TOKS, 2) if headline else None,
+        "dtype": f"fp16/bf16 activations, fp32 accumulate, {wq} weights",
+        "data": f"synthetic uniform-random token ids; random-init {wq} weights ({cfg.name} architecture)",
         "config": {"model": cfg.name, "layers": cfg.n_layers, "global_batch": B, "seq_len": P,
                    "gen_len": G, "parallelism": "single GPU", "kv": "paged fp16, 16-token pages",
-                   "l2": "no flush: 40 GB of weights streamed per step >> 126 MB L2"},
+                   "l2": f"no flush: {eng.model.weight_bytes() / 1e9:.0f} GB of weights per model, "
+                         "streamed per step, >> 126 MB L2"},
         "decode_tok_s_batch1": round(args.steps / (ms1 / 1e3), 2),
         "ms_per_step_batch1": round(ms1 / args.steps, 4),
         "ttft_p50_ms": round(ttft_p50, 2), "ttft_prompt_tokens": P,
@@ -209,16 +216,6 @@ def single_gpu(args):
     if args.layers:
         line["invalid"] = "layer count overridden (debug)"
     print(json.dumps(line), flush=True)
-
-
-def kernel_launches_per_step(model) -> int:
-    """Our kernels per decode forward: embed + rmsnorm, per layer 4 GEMMs +
-    4 epilogues + attention split + combine, then head GEMM + logits copy +
-    row gather + argmax."""
-    n = 2 + 10 * len(model.layers)
-    if model.last:
-        n += 3  # head GEMM, logits epilogue, argmax (the row gather is a torch op)
-    return n
 
 
 def main():

@@ -3,19 +3,16 @@
 
 namespace {
 
-void moe_route(Tensor x, Tensor wr, int64_t wtype, OptT br, int64_t E, int64_t k,
-               bool softmax_after_topk, Tensor ids, Tensor wts, Tensor counts) {
-  CHECK_DT(x, at::kHalf); CHECK_DT(ids, at::kInt); CHECK_DT(wts, at::kFloat);
-  CHECK_DT(counts, at::kInt); CHECK_CUDA(wr); CHECK_CONTIG(wr);
-  TORCH_CHECK(x.stride(-1) == 1, "x rows must be contiguous");
-  const at::cuda::CUDAGuard guard(x.device());
-  const int T = (int)x.size(0);
+void moe_topk(const GemmResult& lg, OptT br, int64_t T, int64_t E, int64_t k,
+              bool softmax_after_topk, Tensor ids, Tensor wts, Tensor counts) {
+  CHECK_DT(ids, at::kInt); CHECK_DT(wts, at::kFloat); CHECK_DT(counts, at::kInt);
+  TORCH_CHECK(lg.g.rows == E && lg.g.T >= T, "router logits shape");
   TORCH_CHECK(ids.numel() >= T * k && wts.numel() >= T * k, "ids/wts too small");
-  int rc = launch_moe_route(reinterpret_cast<const __half*>(x.data_ptr()), (int)x.stride(0), T,
-                            (int)x.size(1), wr.data_ptr(), (int)wtype, ptr_or_null<float>(br),
-                            (int)E, (int)k, softmax_after_topk ? 1 : 0, ids.data_ptr<int32_t>(),
-                            wts.data_ptr<float>(), counts.data_ptr<int>(), cur_stream());
-  TORCH_CHECK(rc == 0, "moe_route failed: rc=", rc);
+  const at::cuda::CUDAGuard guard(ids.device());
+  int rc = launch_moe_topk(lg.g, ptr_or_null<float>(br), (int)T, (int)E, (int)k,
+                           softmax_after_topk ? 1 : 0, ids.data_ptr<int32_t>(),
+                           wts.data_ptr<float>(), counts.data_ptr<int>(), cur_stream());
+  TORCH_CHECK(rc == 0, "moe_topk failed: rc=", rc);
 }
 
 void moe_plan(Tensor counts, int64_t E, int64_t tok_tile, Tensor offsets, Tensor cursor,
@@ -99,7 +96,7 @@ void mxfp4_repack(Tensor src, int64_t rows, int64_t K, Tensor dst) {
 }  // namespace
 
 void register_moe_ops(py::module& m) {
-  m.def("moe_route", &moe_route);
+  m.def("moe_topk", &moe_topk);
   m.def("moe_plan", &moe_plan);
   m.def("moe_scatter", &moe_scatter);
   m.def("moe_gemm", &moe_gemm, py::arg("fmt"), py::arg("epi"), py::arg("w"), py::arg("rows"),

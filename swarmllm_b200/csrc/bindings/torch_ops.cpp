@@ -291,6 +291,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                                   out.data_ptr<float>(), cur_stream());
     TORCH_CHECK(rc == 0, "ssm_conv_silu failed: rc=", rc);
   });
+  m.def("delta_chunk", [](Tensor qkv, int64_t nk, int64_t nv, int64_t D, const GemmResult& gba,
+                          Tensor dt_bias, Tensor A, const GemmResult& gz, Tensor norm_w, double eps,
+                          Tensor state, Tensor seqs, int64_t S, Tensor o_raw, Tensor out) {
+    CHECK_DT(qkv, at::kFloat); CHECK_DT(state, at::kFloat); CHECK_DT(out, at::kHalf);
+    CHECK_DT(o_raw, at::kFloat); CHECK_DT(seqs, at::kInt); CHECK_CONTIG(qkv); CHECK_CONTIG(out);
+    TORCH_CHECK(qkv.size(-1) == (2 * nk + nv) * D, "qkv width");
+    TORCH_CHECK(o_raw.numel() >= out.numel(), "o_raw too small");
+    const at::cuda::CUDAGuard guard(out.device());
+    int rc = launch_delta_chunk(qkv.data_ptr<float>(), (int)qkv.size(-1), (int)nk, (int)nv, (int)D,
+                                gba.g, dt_bias.data_ptr<float>(), A.data_ptr<float>(), gz.g,
+                                norm_w.data_ptr<float>(), (float)eps, state.data_ptr<float>(),
+                                seqs.data_ptr(), (int)S, (int)out.size(0), o_raw.data_ptr<float>(),
+                                reinterpret_cast<__half*>(out.data_ptr()), cur_stream());
+    TORCH_CHECK(rc == 0, "delta_chunk failed: rc=", rc);
+  });
   m.def("delta_rule", [](Tensor qkv, int64_t nk, int64_t nv, int64_t D, const GemmResult& gba,
                          Tensor dt_bias, Tensor A, const GemmResult& gz, Tensor norm_w, double eps,
                          Tensor state, Tensor seqs, int64_t S, Tensor out) {

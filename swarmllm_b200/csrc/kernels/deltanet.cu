@@ -1,8 +1,10 @@
 // Gated DeltaNet (linear attention of the Qwen3-Next-style hybrid) on sm_100a.
 //
 //   ssm_conv_silu   causal depthwise conv1d (kernel 4) over the q|k|v channels
-//                   of the in-projection, with per-sequence carried state, then
-//                   SiLU.  Rows of one sequence are consecutive in the batch.
+//                   of the in-projection, then SiLU: one thread per (row,
+//                   channel), the inputs before the step come from the
+//                   per-sequence carried window, which a second kernel then
+//                   advances.  Rows of one sequence are consecutive in the batch.
 //   delta_rule      the gated delta rule per (sequence, value head), state
 //                   S[dk][dv] in fp32:
 //                     S <- S * exp(g_t)
@@ -27,34 +29,59 @@
 
 namespace swarm {
 
+// Sequence of batch row r (seqs sorted by row0); -1 if r belongs to none.
+SW_DEVICE int seq_of_row(const int4* seqs, int S, int r) {
+  int lo = 0, hi = S - 1, f = -1;
+  while (lo <= hi) {
+    const int m = (lo + hi) >> 1;
+    if (seqs[m].x <= r) { f = m; lo = m + 1; } else { hi = m - 1; }
+  }
+  if (f < 0 || r >= seqs[f].x + seqs[f].y) return -1;
+  return f;
+}
+
+// One thread per (row, channel); inputs before the sequence's first row of
+// this step come from the carried window (zeros at position 0).
 template <int K>
 __global__ void ssm_conv_silu_kernel(GemmOut g, const float* __restrict__ w, int C,
-                                     float* __restrict__ state, const int4* __restrict__ seqs,
+                                     const float* __restrict__ state,
+                                     const int4* __restrict__ seqs, int S,
                                      float* __restrict__ out) {
-  const int s = blockIdx.y;
+  const int r = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
-  const int4 sq = seqs[s];
-  const int r0 = sq.x, n = sq.y, slot = sq.z, p0 = sq.w;
-  if (n <= 0) return;
-  float win[K - 1], wk[K];
+  const int si = seq_of_row(seqs, S, r);
+  if (si < 0) return;
+  const int4 sq = seqs[si];
+  const int l = r - sq.x;
+  float acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < K; ++i) wk[i] = w[(size_t)c * K + i];
-  float* st = state + (size_t)slot * (K - 1) * C;
+  for (int i = 0; i < K; ++i) {
+    const int j = l - (K - 1) + i;  // local index of the input
+    float x;
+    if (j >= 0) x = g.get(sq.x + j, c);
+    else x = sq.w == 0 ? 0.f : state[((size_t)sq.z * (K - 1) + (K - 1) + j) * C + c];
+    acc += w[(size_t)c * K + i] * x;
+  }
+  out[(size_t)r * C + c] = silu(acc);
+}
+
+// After the conv: each sequence's window <- its last K-1 inputs.
+template <int K>
+__global__ void ssm_conv_state_kernel(GemmOut g, int C, float* __restrict__ state,
+                                      const int4* __restrict__ seqs) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int4 sq = seqs[blockIdx.y];
+  if (c >= C || sq.y <= 0) return;
+  float* st = state + (size_t)sq.z * (K - 1) * C;
+  float nw[K - 1];
 #pragma unroll
-  for (int i = 0; i < K - 1; ++i) win[i] = p0 == 0 ? 0.f : st[(size_t)i * C + c];
-  for (int t = 0; t < n; ++t) {
-    const float v = g.get(r0 + t, c);
-    float acc = wk[K - 1] * v;
-#pragma unroll
-    for (int i = 0; i < K - 1; ++i) acc += wk[i] * win[i];
-#pragma unroll
-    for (int i = 0; i < K - 2; ++i) win[i] = win[i + 1];
-    win[K - 2] = v;
-    out[(size_t)(r0 + t) * C + c] = silu(acc);
+  for (int i = 0; i < K - 1; ++i) {
+    const int j = sq.y - (K - 1) + i;
+    nw[i] = j >= 0 ? g.get(sq.x + j, c) : (sq.w == 0 ? 0.f : st[(size_t)((K - 1) + j) * C + c]);
   }
 #pragma unroll
-  for (int i = 0; i < K - 1; ++i) st[(size_t)i * C + c] = win[i];
+  for (int i = 0; i < K - 1; ++i) st[(size_t)i * C + c] = nw[i];
 }
 
 // Block-wide sums of two values for a 128-thread block (4 warps).
@@ -137,10 +164,12 @@ using namespace swarm;
 
 int launch_ssm_conv_silu(const GemmOut& g, const float* w, int C, int K, float* state,
                          const void* seqs, int S, float* out, cudaStream_t s) {
-  if (S <= 0) return 0;
+  if (S <= 0 || g.T <= 0) return 0;
   if (K != 4) return -1;
-  dim3 grid((C + 127) / 128, S);
-  ssm_conv_silu_kernel<4><<<grid, 128, 0, s>>>(g, w, C, state, (const int4*)seqs, out);
+  ssm_conv_silu_kernel<4><<<dim3((C + 127) / 128, g.T), 128, 0, s>>>(g, w, C, state,
+                                                                      (const int4*)seqs, S, out);
+  ssm_conv_state_kernel<4><<<dim3((C + 127) / 128, S), 128, 0, s>>>(g, C, state,
+                                                                   (const int4*)seqs);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }
 

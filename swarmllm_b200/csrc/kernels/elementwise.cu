@@ -76,9 +76,12 @@ __global__ void epi_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ resid
     out[(size_t)t * out_stride + i] = __float2half_rn(row[i] * inv * w[i]);
 }
 
-// One CTA per token; threads walk (head, pair).  Layout of the QKV GEMM rows:
-// [q heads][k heads][v heads], each head_dim wide.
+// Grid (token, group of kRopeHpb heads) over the head list [q | k | v].
+// Layout of the QKV GEMM rows: [q heads][k heads][v heads], each head_dim
+// wide -- or, for gated attention, each q head as [q | gate].
 // Cache layout: [pages][n_kv][page_size][head_dim] fp16.
+constexpr int kRopeHpb = 4;
+
 __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
                                    const int32_t* __restrict__ positions,
                                    const int32_t* __restrict__ slots,
@@ -89,58 +92,57 @@ __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
                                    const float* __restrict__ q_norm_w,
                                    const float* __restrict__ k_norm_w, float norm_eps,
                                    __half* __restrict__ gate_out) {
-  extern __shared__ float sh[];  // (n_q + n_kv) * head_dim floats
+  extern __shared__ float sh[];  // kRopeHpb * head_dim floats
   const int t = blockIdx.x;
+  const int h0 = blockIdx.y * kRopeHpb;
+  const int n_heads = n_q + 2 * n_kv;
+  const int nh = min(kRopeHpb, n_heads - h0);
   const int pos = positions[t];
   const int slot = slots ? slots[t] : -1;
-  const int qk_rows = (n_q + n_kv) * head_dim;
-  const int total = (n_q + 2 * n_kv) * head_dim;
+  const int page = slot >= 0 ? slot / page_size : 0, off = slot >= 0 ? slot - page * page_size : 0;
   const int q_rows = n_q * head_dim;
-  // Gated attention: each q head's GEMM rows are [q (head_dim) | gate (head_dim)];
-  // sigmoid(gate) goes to gate_out for the multiply after attention.
-  if (gate_out != nullptr) {
-    for (int i = threadIdx.x; i < q_rows; i += blockDim.x) {
-      const int h = i / head_dim, d = i - h * head_dim;
-      const float gv = g.get(t, h * 2 * head_dim + head_dim + d);
-      gate_out[(size_t)t * q_rows + i] = __float2half_rn(1.f / (1.f + __expf(-gv)));
-    }
-  }
-  // Stage q and k (pre-RoPE) in shared memory; write v straight to the cache.
-  for (int i = threadIdx.x; i < total; i += blockDim.x) {
-    int gr = i;  // GEMM row of logical row i
-    if (gate_out != nullptr) {
-      const int h = i / head_dim;
-      gr = (i < q_rows) ? i + h * head_dim : i + q_rows;
-    }
-    float v = g.get(t, gr) + (bias ? bias[i] : 0.f);
-    if (i < qk_rows) {
+  const bool gated = gate_out != nullptr;
+  // Stage this CTA's q/k heads (pre-RoPE) in shared memory; v goes straight to the cache.
+  for (int i = threadIdx.x; i < nh * head_dim; i += blockDim.x) {
+    const int hh = h0 + i / head_dim, d = i - (i / head_dim) * head_dim;
+    const int lr = hh * head_dim + d;  // logical row
+    const int gr = gated ? (hh < n_q ? lr + hh * head_dim : lr + q_rows) : lr;
+    const float v = g.get(t, gr) + (bias ? bias[lr] : 0.f);
+    if (hh < n_q + n_kv) {
       sh[i] = v;
+      if (gated && hh < n_q) {
+        const float gv = g.get(t, gr + head_dim);
+        gate_out[(size_t)t * q_rows + lr] = __float2half_rn(1.f / (1.f + __expf(-gv)));
+      }
     } else if (slot >= 0) {
-      const int j = i - qk_rows, h = j / head_dim, d = j - h * head_dim;
-      const int page = slot / page_size, off = slot - page * page_size;
-      v_cache[(((size_t)page * n_kv + h) * page_size + off) * head_dim + d] = __float2half_rn(v);
+      const int hv = hh - n_q - n_kv;
+      v_cache[(((size_t)page * n_kv + hv) * page_size + off) * head_dim + d] = __float2half_rn(v);
     }
   }
   __syncthreads();
   // Optional per-head RMSNorm of q and k (Qwen3-style qk-norm); one warp per head.
   if (q_norm_w != nullptr) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int h = warp; h < n_q + n_kv; h += nw) {
-      float* x = sh + h * head_dim;
-      float s = 0.f;
-      for (int d = lane; d < head_dim; d += 32) s += x[d] * x[d];
-      s = warp_sum(s);
-      const float inv = rsqrtf(s / head_dim + norm_eps);
-      const float* wn = (h < n_q) ? q_norm_w : k_norm_w;
+    for (int j = warp; j < nh; j += nw) {
+      const int hh = h0 + j;
+      if (hh >= n_q + n_kv) continue;
+      float* x = sh + j * head_dim;
+      float ss = 0.f;
+      for (int d = lane; d < head_dim; d += 32) ss += x[d] * x[d];
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / head_dim + norm_eps);
+      const float* wn = (hh < n_q) ? q_norm_w : k_norm_w;
       for (int d = lane; d < head_dim; d += 32) x[d] = x[d] * inv * wn[d];
     }
     __syncthreads();
   }
   const int half = rope_dim / 2;
   // Rotate pairs; unrotated tail dims are copied.
-  for (int i = threadIdx.x; i < (n_q + n_kv) * head_dim; i += blockDim.x) {
-    const int h = i / head_dim, d = i - h * head_dim;
-    const float* x = sh + h * head_dim;
+  for (int i = threadIdx.x; i < nh * head_dim; i += blockDim.x) {
+    const int j = i / head_dim, d = i - j * head_dim;
+    const int hh = h0 + j;
+    if (hh >= n_q + n_kv) continue;
+    const float* x = sh + j * head_dim;
     float y;
     if (d < rope_dim) {
       int fi, partner;
@@ -154,19 +156,18 @@ __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
         first = (d & 1) == 0;
         partner = first ? d + 1 : d - 1;
       }
-      float s, c;
-      sincosf((float)pos * inv_freq[fi], &s, &c);
-      c *= attn_factor;
-      s *= attn_factor;
-      y = first ? (x[d] * c - x[partner] * s) : (x[partner] * s + x[d] * c);
+      float sn, cs;
+      sincosf((float)pos * inv_freq[fi], &sn, &cs);
+      cs *= attn_factor;
+      sn *= attn_factor;
+      y = first ? (x[d] * cs - x[partner] * sn) : (x[partner] * sn + x[d] * cs);
     } else {
       y = x[d];
     }
-    if (h < n_q) {
-      q_out[((size_t)t * n_q + h) * head_dim + d] = __float2half_rn(y);
+    if (hh < n_q) {
+      q_out[((size_t)t * n_q + hh) * head_dim + d] = __float2half_rn(y);
     } else if (slot >= 0) {
-      const int hk = h - n_q;
-      const int page = slot / page_size, off = slot - page * page_size;
+      const int hk = hh - n_q;
       k_cache[(((size_t)page * n_kv + hk) * page_size + off) * head_dim + d] = __float2half_rn(y);
     }
   }
@@ -254,14 +255,11 @@ void launch_epi_rope_kv(const GemmOut& g, const float* bias, const int32_t* posi
                         const float* q_norm_w, const float* k_norm_w, float norm_eps,
                         __half* gate_out, cudaStream_t s) {
   if (g.T <= 0) return;
-  size_t sm = (size_t)(n_q + n_kv) * head_dim * sizeof(float);
-  if (sm > 48 * 1024)
-    cudaFuncSetAttribute(epi_rope_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)sm);
-  epi_rope_kv_kernel<<<g.T, 256, sm, s>>>(g, bias, positions, slots, inv_freq, n_q, n_kv,
-                                          head_dim, rope_dim, neox, attn_factor, q_out, k_cache,
-                                          v_cache, page_size, q_norm_w, k_norm_w, norm_eps,
-                                          gate_out);
+  const size_t sm = (size_t)kRopeHpb * head_dim * sizeof(float);
+  const int groups = (n_q + 2 * n_kv + kRopeHpb - 1) / kRopeHpb;
+  epi_rope_kv_kernel<<<dim3(g.T, groups), 128, sm, s>>>(
+      g, bias, positions, slots, inv_freq, n_q, n_kv, head_dim, rope_dim, neox, attn_factor,
+      q_out, k_cache, v_cache, page_size, q_norm_w, k_norm_w, norm_eps, gate_out);
   SW_LAUNCH_CHECK();
 }
 

@@ -89,9 +89,8 @@ int moe_tok_tile(int pairs, int n_experts);
 int moe_max_tiles(int pairs, int n_experts, int tok_tile);
 long long moe_packed_bytes(int fmt, int rows, int K);
 int launch_mxfp4_repack(const void* src, int rows, int K, void* dst, cudaStream_t s);
-int launch_moe_route(const __half* x, int x_stride, int T, int H, const void* wr, int wtype,
-                     const float* br, int E, int k, int softmax_after_topk, int32_t* ids,
-                     float* wts, int* counts, cudaStream_t s);
+int launch_moe_topk(const swarm::GemmOut& lg, const float* br, int T, int E, int k,
+                    int softmax_after_topk, int32_t* ids, float* wts, int* counts, cudaStream_t s);
 int launch_moe_plan(int* counts, int E, int tok_tile, int* offsets, int* cursor, void* tiles,
                     int* n_tiles, int max_tiles, int* status, cudaStream_t s);
 int launch_moe_scatter(const __half* x, int x_stride, int H, const int32_t* ids, int P, int k,
@@ -118,3 +117,7 @@ int launch_delta_rule(const float* qkv, int C, int nk, int nv, int D, const swar
                       const float* dt_bias, const float* A, const swarm::GemmOut& gz,
                       const float* norm_w, float eps, float* state, const void* seqs, int S,
                       __half* out, cudaStream_t s);
+int launch_delta_chunk(const float* qkv, int C, int nk, int nv, int D, const swarm::GemmOut& gba,
+                       const float* dt_bias, const float* A, const swarm::GemmOut& gz,
+                       const float* norm_w, float eps, float* state, const void* seqs, int S,
+                       int T, float* o_raw, __half* out, cudaStream_t s);

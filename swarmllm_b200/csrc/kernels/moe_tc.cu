@@ -1,8 +1,8 @@
 // Mixture-of-experts FFN on sm_100a: routing, token dispatch, grouped expert
 // GEMMs on the 5th-generation tensor cores, and the weighted combine.
 //
-//   moe_route    router GEMV (+bias) fused with top-k selection and the
-//                routing weights; per-expert token counts          (B8 front)
+//   moe_topk     router logits (a tensor-core GEMM result) + bias -> top-k
+//                selection, routing weights, per-expert token counts (B8 front)
 //   moe_plan     one CTA: per-expert offsets (exclusive scan) and the list of
 //                (expert, token-tile) work tiles, all on the device so the
 //                whole layer is CUDA-graph capturable
@@ -43,57 +43,28 @@ constexpr int kMoeEpiStore = 1;
 constexpr int kMxUnitBytes = 128 * kMxRowBytes;  // 17408
 
 // ============================================================== routing
-// One CTA = kTpb tokens; warp w computes router logits for experts w, w+8, ...
-// over the kTpb token rows staged in shared memory, then warp t selects the
-// top-k of token t.
-constexpr int kRouteTpb = 8;
-
-SW_DEVICE float load_w(const uint8_t* row, int type, int i) {
-  if (type == GGML_F32) return reinterpret_cast<const float*>(row)[i];
-  if (type == GGML_F16) return __half2float(reinterpret_cast<const __half*>(row)[i]);
-  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(row)[i]);
-}
-
-__global__ void __launch_bounds__(256) moe_route_kernel(
-    const __half* __restrict__ x, int x_stride, int T, int H, const uint8_t* __restrict__ wr,
-    int wtype, const float* __restrict__ br, int E, int k, int softmax_after_topk,
-    int32_t* __restrict__ ids, float* __restrict__ wts, int* __restrict__ counts) {
-  extern __shared__ __align__(16) uint8_t route_smem[];
-  __half* xs = reinterpret_cast<__half*>(route_smem);                      // [kTpb][H]
-  float* lg = reinterpret_cast<float*>(route_smem + kRouteTpb * H * 2);  // [kTpb][E]
-  const int t0 = blockIdx.x * kRouteTpb;
-  const int nt = min(kRouteTpb, T - t0);
-  for (int i = threadIdx.x; i < kRouteTpb * H; i += blockDim.x) {
-    const int tk = i / H, c = i - tk * H;
-    xs[i] = tk < nt ? x[(size_t)(t0 + tk) * x_stride + c] : __float2half(0.f);
-  }
+// Router logits come from a tensor-core GEMM (any GemmOut).  One CTA per
+// token: all threads read the (split-K) logits in parallel into shared
+// memory, then warp 0 adds nothing more than the selection: top-k (ties ->
+// lower expert id), routing weights, per-expert token counts.
+__global__ void __launch_bounds__(256) moe_topk_kernel(GemmOut lg, const float* __restrict__ br,
+                                                       int T, int E, int k, int softmax_after_topk,
+                                                       int32_t* __restrict__ ids,
+                                                       float* __restrict__ wts,
+                                                       int* __restrict__ counts) {
+  __shared__ float lgs[512];
+  const int t = blockIdx.x;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) lgs[e] = lg.get(t, e) + (br ? br[e] : 0.f);
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t wbytes = wtype == GGML_F32 ? 4 : 2;
-  for (int e = warp; e < E; e += 8) {
-    const uint8_t* row = wr + (size_t)e * H * wbytes;
-    float acc[kRouteTpb];
-#pragma unroll
-    for (int tk = 0; tk < kRouteTpb; ++tk) acc[tk] = 0.f;
-    for (int c = lane; c < H; c += 32) {
-      const float wv = load_w(row, wtype, c);
-#pragma unroll
-      for (int tk = 0; tk < kRouteTpb; ++tk) acc[tk] += wv * __half2float(xs[tk * H + c]);
-    }
-#pragma unroll
-    for (int tk = 0; tk < kRouteTpb; ++tk) {
-      const float v = warp_sum(acc[tk]);
-      if (lane == 0) lg[tk * E + e] = v + (br ? br[e] : 0.f);
-    }
-  }
-  __syncthreads();
-  if (warp >= nt) return;
-  // ---- top-k of token `warp` (ties -> lower expert id)
-  const float* l = lg + warp * E;
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
   constexpr int kMaxPer = 16;  // E <= 512
   float v[kMaxPer];
 #pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) v[i] = (lane + 32 * i < E) ? l[lane + 32 * i] : -INFINITY;
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? lgs[e] : -INFINITY;
+  }
   float sel_v = 0.f, top = 0.f, denom_all = 0.f;
   int sel_e = 0;
   for (int j = 0; j < k; ++j) {
@@ -111,11 +82,11 @@ __global__ void __launch_bounds__(256) moe_route_kernel(
     if (j == 0) {
       top = bv;
       if (!softmax_after_topk) {  // softmax over all experts, then pick
-        float s = 0.f;
+        float sum = 0.f;
 #pragma unroll
         for (int i = 0; i < kMaxPer; ++i)
-          if (lane + 32 * i < E) s += __expf(v[i] - top);
-        denom_all = warp_sum(s);
+          if (lane + 32 * i < E) sum += __expf(v[i] - top);
+        denom_all = warp_sum(sum);
       }
     }
     if (be >= E) be = 0;  // only reachable with NaN logits
@@ -129,7 +100,7 @@ __global__ void __launch_bounds__(256) moe_route_kernel(
   const float ex = lane < k ? __expf(sel_v - top) : 0.f;
   const float denom = softmax_after_topk ? warp_sum(ex) : denom_all;
   if (lane < k) {
-    const size_t o = (size_t)(t0 + warp) * k + lane;
+    const size_t o = (size_t)t * k + lane;
     ids[o] = sel_e;
     wts[o] = ex / denom;
     atomicAdd(&counts[sel_e], 1);
@@ -607,23 +578,11 @@ int launch_mxfp4_repack(const void* src, int rows, int K, void* dst, cudaStream_
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }
 
-int launch_moe_route(const __half* x, int x_stride, int T, int H, const void* wr, int wtype,
-                     const float* br, int E, int k, int softmax_after_topk, int32_t* ids,
-                     float* wts, int* counts, cudaStream_t s) {
+int launch_moe_topk(const GemmOut& lg, const float* br, int T, int E, int k,
+                    int softmax_after_topk, int32_t* ids, float* wts, int* counts, cudaStream_t s) {
   if (T <= 0) return 0;
   if (E > 512 || k > 32 || k > E) return -1;
-  if (wtype != GGML_F32 && wtype != GGML_F16 && wtype != GGML_BF16) return -2;
-  const size_t smem = (size_t)kRouteTpb * H * 2 + (size_t)kRouteTpb * E * 4;
-  if (smem > 200 * 1024) return -3;
-  static size_t attr = 0;
-  if (smem > 48 * 1024 && smem > attr) {
-    cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-    attr = smem;
-  }
-  moe_route_kernel<<<(T + kRouteTpb - 1) / kRouteTpb, 256, smem, s>>>(
-      x, x_stride, T, H, (const uint8_t*)wr, wtype, br, E, k, softmax_after_topk, ids, wts,
-      counts);
+  moe_topk_kernel<<<T, 256, 0, s>>>(lg, br, T, E, k, softmax_after_topk, ids, wts, counts);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

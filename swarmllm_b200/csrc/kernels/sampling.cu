@@ -84,6 +84,48 @@ SW_DEVICE ArgMax block_argmax(ArgMax x, float* sv, int* si) {
   return ArgMax{sv[0], si[0]};
 }
 
+// Split argmax for few rows over a large vocabulary: a grid of (row, slice)
+// CTAs each merge their slice's winner into one 64-bit key per row with
+// atomicMax -- order-preserving image of the float in the high word, the
+// complemented index in the low word (ties -> lower index) -- and a second
+// kernel unpacks it and clears the key for the next use.
+constexpr int kArgmaxMaxRows = 4096;
+__device__ unsigned long long g_argmax_keys[kArgmaxMaxRows];
+
+SW_DEVICE uint32_t float_order_bits(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(256) argmax_split_kernel(const float* __restrict__ logits, int V,
+                                                           int stride, int slice) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int row = blockIdx.x;
+  const float* r = logits + (size_t)row * stride;
+  const int lo = blockIdx.y * slice, hi = min(V, lo + slice);
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) best = argmax_merge(best, ArgMax{r[i], i});
+  best = block_argmax(best, sv, si);
+  if (threadIdx.x == 0 && best.i != 0x7fffffff) {
+    const unsigned long long key = ((unsigned long long)float_order_bits(best.v) << 32) |
+                                   (unsigned long long)(0xFFFFFFFFu - (uint32_t)best.i);
+    atomicMax(&g_argmax_keys[row], key);
+  }
+}
+
+__global__ void argmax_finish_kernel(int rows, int32_t* __restrict__ out, float* __restrict__ out_val) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const unsigned long long key = g_argmax_keys[row];
+  g_argmax_keys[row] = 0ull;
+  out[row] = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+  if (out_val) {
+    const uint32_t hb = (uint32_t)(key >> 32);
+    out_val[row] = __uint_as_float((hb & 0x80000000u) ? (hb & 0x7FFFFFFFu) : ~hb);
+  }
+}
+
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V,
                                                       int stride, int32_t* __restrict__ out,
                                                       float* __restrict__ out_val) {
@@ -213,7 +255,17 @@ using namespace swarm;
 void launch_argmax(const float* logits, int rows, int V, int stride, int32_t* out, float* out_val,
                    cudaStream_t s) {
   if (rows <= 0) return;
-  argmax_kernel<<<rows, 1024, 0, s>>>(logits, V, stride, out, out_val);
+  // Few rows over a big vocabulary: spread each row over ~2 waves of CTAs.
+  // (The per-row keys are one static buffer: argmax launches on different
+  // streams of one device must not overlap.)
+  const int splits = rows >= 296 ? 1 : (296 + rows - 1) / rows;
+  if (splits > 1 && V >= 8192 && rows <= kArgmaxMaxRows) {
+    const int sl = ((V + splits - 1) / splits + 255) / 256 * 256;
+    argmax_split_kernel<<<dim3(rows, (V + sl - 1) / sl), 256, 0, s>>>(logits, V, stride, sl);
+    argmax_finish_kernel<<<(rows + 127) / 128, 128, 0, s>>>(rows, out, out_val);
+  } else {
+    argmax_kernel<<<rows, 1024, 0, s>>>(logits, V, stride, out, out_val);
+  }
   SW_LAUNCH_CHECK();
 }
 

@@ -159,8 +159,8 @@ class GpuRunner:
         n = len(table)
         m = max(n, pad_to)
         self.h_ssm[:n] = torch.from_numpy(table)
-        if m > n:  # padding sequences: no rows
-            self.h_ssm[n:m, 0] = 0
+        if m > n:  # padding sequences: no rows; row0 past every real row keeps the table sorted
+            self.h_ssm[n:m, 0] = torch.arange(1 << 30, (1 << 30) + m - n, dtype=torch.int32)
             self.h_ssm[n:m, 1] = 0
             self.h_ssm[n:m, 2] = self.slots.trash
             self.h_ssm[n:m, 3] = 0
@@ -203,7 +203,8 @@ class GpuRunner:
         self.d_bt[:B] = self.trash_page
         self.d_samp[:B] = torch.arange(B, device=self.device)
         if self.slots is not None:
-            self.d_ssm[:B, 0] = torch.arange(B, device=self.device, dtype=torch.int32)
+            self.d_ssm[:B, 0] = torch.arange(1 << 30, (1 << 30) + B, device=self.device,
+                                             dtype=torch.int32)
             self.d_ssm[:B, 1] = 0
             self.d_ssm[:B, 2] = self.slots.trash
             self.d_ssm[:B, 3] = 0
@@ -230,6 +231,8 @@ class GpuRunner:
             M, _ = self._upload(tokens, positions, slots, bt_rows, seq_lens, sample_rows)
             ns = self._upload_ssm(table) if table is not None else 0
             b = self._batch(M, S, ns)
+            if table is not None and len(table):
+                b.ssm_max_rows = int(table[:, 1].max())
             cfg = self.model.cfg
             grp = attention_groups(plan, cfg.n_heads // cfg.n_kv_heads)
             if grp is not None:

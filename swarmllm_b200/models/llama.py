@@ -28,7 +28,7 @@ import torch
 from ..gguf import quants as Q
 from ..ops.attention import AttentionWorkspace, PagedKVCache, paged_attention
 from ..ops.linear import GemmWorkspace, QLinear
-from ..ops.moe import MoeExperts, MoeWorkspace, moe_ffn
+from ..ops.moe import MoeExperts, MoeWorkspace, moe_experts, moe_route
 from ..utils.ext import C
 from .config import ModelConfig, rope_inv_freq
 
@@ -47,6 +47,7 @@ class StepBatch:
     tree_start: torch.Tensor | None = None  # int32 [N]
     groups: tuple | None = None             # (row0 int32[G], npos int32[G], positions/group)
     ssm_seqs: torch.Tensor | None = None    # int32 [S, 4] (row0, nrows, state slot, pos0): linear attention
+    ssm_max_rows: int = 1                   # host hint: most rows of one sequence in this step
 
 
 def _f32(t: torch.Tensor, qt: int, shape) -> torch.Tensor:
@@ -144,7 +145,7 @@ class LlamaGPU:
         t, qt, shape = get(b + "attn_gate.weight")
         L.w_z = QLinear(t, qt, shape[0], H, dev)
         t, qt, shape = get(b + "ssm_ba.weight")
-        L.w_ba = QLinear(t, qt, 2 * nv, H, dev)
+        L.w_ba = QLinear(t, qt, 2 * nv, H, dev, f32_as_f16=True)
         L.conv_w = small(b + "ssm_conv1d.weight").contiguous()
         L.dt_bias = small(b + "ssm_dt.bias")
         L.A = small(b + "ssm_a")
@@ -180,7 +181,7 @@ class LlamaGPU:
                                limit=cfg.swiglu_limit, **biases)
         del g, u, d
         t, rq, _ = get(b + "ffn_gate_inp.weight")
-        L.router, L.router_type = t.contiguous(), rq
+        L.router = QLinear(t, rq, E, H, dev, f32_as_f16=True)
         L.router_b = small(b + "ffn_gate_inp.bias") if cfg.arch == "gpt-oss" else None
         L.sh_gu = L.sh_down = L.sh_gate = None
         if cfg.shared_expert_ffn:
@@ -190,7 +191,7 @@ class LlamaGPU:
             t, qt2, shape = get(b + "ffn_down_shexp.weight")
             L.sh_down = QLinear(t, qt2, shape[0], shape[1], dev)
             t, qt3, _ = get(b + "ffn_gate_inp_shexp.weight")
-            L.sh_gate = QLinear(t, qt3, 1, H, dev)
+            L.sh_gate = QLinear(t, qt3, 1, H, dev, f32_as_f16=True)
 
     def _linears(self):
         for L in self.layers:
@@ -218,8 +219,6 @@ class LlamaGPU:
                 2 * c.shared_expert_ffn)
         if self.n_lin_layers:
             r = max(r, (2 * c.ssm_k_heads + c.ssm_v_heads) * c.ssm_head_dim)
-        if self.last:
-            r = max(r, c.vocab)
         return r
 
     def _deltanet(self, L, b, kv, ctx, x, N):
@@ -229,10 +228,31 @@ class LlamaGPU:
         S = b.ssm_seqs.shape[0]
         g = L.w_in(x, ctx.gemm)
         C().ssm_conv_silu(g, L.conv_w, kv.conv_state(L.lin_idx), b.ssm_seqs, S, ctx.ssm_qkv[:N])
-        gba = L.w_ba(x, ctx.gemm, out=ctx.ssm_ba[:N])
+        gba = L.w_ba(x, ctx.gemm_side)
         gz = L.w_z(x, ctx.gemm)  # the conv consumed the in-projection's workspace already
-        C().delta_rule(ctx.ssm_qkv[:N], nk, nv, dh, gba, L.dt_bias, L.A, gz, L.ssm_norm,
-                       cfg.rms_eps, kv.ssm_state(L.lin_idx), b.ssm_seqs, S, ctx.ssm_out[:N])
+        if b.ssm_max_rows > 32:  # prefill: chunked evaluation
+            C().delta_chunk(ctx.ssm_qkv[:N], nk, nv, dh, gba, L.dt_bias, L.A, gz, L.ssm_norm,
+                            cfg.rms_eps, kv.ssm_state(L.lin_idx), b.ssm_seqs, S,
+                            ctx.ssm_oraw[:N], ctx.ssm_out[:N])
+        else:
+            C().delta_rule(ctx.ssm_qkv[:N], nk, nv, dh, gba, L.dt_bias, L.A, gz, L.ssm_norm,
+                           cfg.rms_eps, kv.ssm_state(L.lin_idx), b.ssm_seqs, S, ctx.ssm_out[:N])
+
+    def decode_launches(self) -> int:
+        """Kernels of this stage's decode forward (what a captured graph replays)."""
+        n = 2 if self.first else 1  # embed + rmsnorm (or the residual copy)
+        for L in self.layers:
+            if L.linear:
+                n += 7   # in GEMM, conv, ba GEMM, z GEMM, delta rule, out GEMM, residual+norm
+            else:
+                n += 6 + (1 if L.gated else 0)  # qkv GEMM, rope/KV, attention + combine, o GEMM, residual+norm
+            if L.experts is not None:
+                n += 6 + (4 if L.sh_gu is not None else 0)
+            else:
+                n += 4   # gate|up GEMM, SwiGLU, down GEMM, residual+norm
+        if self.last:
+            n += 3       # head GEMM, logits copy, argmax (the row gather is a torch op)
+        return n
 
     def make_context(self, max_tokens: int, max_samples: int, max_len: int):
         return GpuForwardContext(self, max_tokens, max_samples, max_len)
@@ -279,15 +299,17 @@ class LlamaGPU:
             else:
                 nxt_w, nxt_out = None, None
             if L.experts is not None:
+                # router logits live in the side workspace only until top-k
+                moe_route(x, L.router, L.router_b, ctx.moe, ctx.gemm_side,
+                          cfg.moe_softmax_after_topk)
                 sh = shg = None
                 if L.sh_gu is not None:
                     S = cfg.shared_expert_ffn
                     g = L.sh_gu(x, ctx.gemm)
                     C().epi_swiglu(g, None, S, 0, False, 0.0, 0.0, ctx.act_sh[:N])
-                    shg = L.sh_gate(x, ctx.gemm, out=ctx.sh_gate[:N])
+                    shg = L.sh_gate(x, ctx.gemm_side)
                     sh = L.sh_down(ctx.act_sh[:N], ctx.gemm)
-                moe_ffn(x, L.experts, L.router, L.router_type, L.router_b, ctx.moe, h, nxt_w,
-                        nxt_out, cfg.rms_eps, cfg.moe_softmax_after_topk, sh, shg)
+                moe_experts(x, L.experts, ctx.moe, h, nxt_w, nxt_out, cfg.rms_eps, sh, shg)
                 continue
             g = L.wgu(x, ctx.gemm)
             C().epi_swiglu(g, None, cfg.ffn, 0, False, 0.0, 0.0, act)
@@ -311,7 +333,12 @@ class GpuForwardContext:
     def __init__(self, model: LlamaGPU, max_tokens: int, max_samples: int, max_len: int):
         cfg, dev = model.cfg, model.device
         self.max_tokens, self.max_samples = max_tokens, max_samples
-        self.gemm = GemmWorkspace(dev, max_tokens, model.max_gemm_rows())
+        head = ((max_samples, cfg.vocab),) if model.last else ()
+        self.gemm = GemmWorkspace(dev, max_tokens, model.max_gemm_rows(), extra=head)
+        # small side GEMMs whose results must outlive a main GEMM issued after
+        # them (router logits, shared-expert gate, DeltaNet beta/decay)
+        side_rows = max(cfg.n_experts, 2 * cfg.ssm_v_heads, 1)
+        self.gemm_side = GemmWorkspace(dev, max_tokens, side_rows, self.gemm.num_sms)
         self.attn = AttentionWorkspace(dev, max_tokens, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
                                        max_len, self.gemm.num_sms)
         H = cfg.hidden
@@ -329,8 +356,8 @@ class GpuForwardContext:
             nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
             self.ssm_qkv = torch.zeros(max_tokens, (2 * nk + nv) * dh, dtype=torch.float32,
                                        device=dev)
-            self.ssm_ba = torch.zeros(max_tokens, 2 * nv, dtype=torch.float32, device=dev)
             self.ssm_out = torch.zeros(max_tokens, nv * dh, dtype=torch.float16, device=dev)
+            self.ssm_oraw = torch.zeros(max_tokens, nv * dh, dtype=torch.float32, device=dev)
         self.moe = None
         if cfg.n_experts:
             ex = next(L.experts for L in model.layers if L.experts is not None)
@@ -338,9 +365,9 @@ class GpuForwardContext:
                                     cfg.n_experts_used, ex.x_dtype, self.gemm.num_sms)
             S = max(cfg.shared_expert_ffn, 1)
             self.act_sh = torch.zeros(max_tokens, S, dtype=torch.float16, device=dev)
-            self.sh_gate = torch.zeros(max_tokens, 1, dtype=torch.float32, device=dev)
         # Size the CUDA-core GEMM scratch up front (graph capture cannot grow it).
-        self.gemm.dense(max_tokens * model.max_gemm_rows() if _has_simt(model) else 0)
+        self.gemm.dense(max(max_tokens * model.max_gemm_rows(),
+                            max_samples * cfg.vocab if model.last else 0) if _has_simt(model) else 0)
 
 
 def _has_simt(model: LlamaGPU) -> bool:

@@ -25,18 +25,23 @@ class GemmWorkspace:
     """Scratch shared by every GEMM of one forward: the stream-K partial
     buffer, a dense fallback buffer and the kernel status word."""
 
-    def __init__(self, device, max_tokens: int, max_rows: int, num_sms: int | None = None):
+    def __init__(self, device, max_tokens: int, max_rows: int, num_sms: int | None = None,
+                 extra: tuple = ()):
+        """Sized for every GEMM of up to `max_tokens` rows x `max_rows`
+        outputs, plus each (tokens, rows) pair in `extra` (e.g. the LM head,
+        which only sees the sampled rows)."""
         self.device = torch.device(device)
         props = torch.cuda.get_device_properties(self.device)
         self.num_sms = num_sms or props.multi_processor_count
         # Stream-K slots: (tiles + CTAs) x tok_tile x 128 floats, CTAs <= num_sms.
         need = 0
-        for T in sorted({1, 16, 32, 64, 128, 256, max_tokens}):
-            if T > max_tokens:
-                continue
-            n_tok = C().q4k_tc_plan(128, 256, T, self.num_sms)[0]
-            tiles = (max_rows + 127) // 128 * ((T + n_tok - 1) // n_tok)
-            need = max(need, (tiles + self.num_sms) * n_tok * 128)
+        for mt, rows in ((max_tokens, max_rows),) + tuple(extra):
+            for T in sorted({1, 16, 32, 64, 128, 256, mt}):
+                if T > mt:
+                    continue
+                n_tok = C().q4k_tc_plan(128, 256, T, self.num_sms)[0]
+                tiles = (rows + 127) // 128 * ((T + n_tok - 1) // n_tok)
+                need = max(need, (tiles + self.num_sms) * n_tok * 128)
         self.ws = torch.empty(int(need), dtype=torch.float32, device=self.device)
         self._dense = torch.empty(0, dtype=torch.float32, device=self.device)
         self.status = torch.zeros(8, dtype=torch.int32, device=self.device)
@@ -62,7 +67,10 @@ class GemmWorkspace:
 
 class QLinear:
     def __init__(self, data, qtype: int, rows: int, K: int, device, bias: np.ndarray | None = None,
-                 force_simt: bool = False):
+                 force_simt: bool = False, f32_as_f16: bool = False):
+        """`f32_as_f16`: run an F32 matrix on the fp16 tensor-core GEMM (for
+        small side projections -- routers, gates -- whose precision needs are
+        met by fp16 weights with fp32 accumulation)."""
         self.qtype, self.rows, self.K = qtype, rows, K
         self.device = torch.device(device)
         raw = data if isinstance(data, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(data))
@@ -76,11 +84,13 @@ class QLinear:
             self.packed = torch.empty(rows * (K // 256) * 144, dtype=torch.uint8, device=self.device)
             C().q4k_repack(raw, rows, K, self.packed)
             self.raw = None
-        elif not force_simt and qtype in (Q.F16, Q.BF16) and K % 8 == 0:
+        elif not force_simt and (qtype in (Q.F16, Q.BF16) or (qtype == Q.F32 and f32_as_f16)) \
+                and K % 8 == 0:
             # 16-bit weights run on the dense tensor-core GEMM in fp16 (exact
             # for F16; BF16 rounds the mantissa, kept only when no weight
             # exceeds the fp16 range).
-            src = raw.view(torch.float16 if qtype == Q.F16 else torch.bfloat16).view(rows, K)
+            dt = {Q.F16: torch.float16, Q.BF16: torch.bfloat16, Q.F32: torch.float32}[qtype]
+            src = raw.view(dt).view(rows, K)
             if qtype == Q.F16 or float(src.float().abs().max()) < 60000.0:
                 self.kind = "dense"
                 self.w16 = src.to(torch.float16).contiguous()

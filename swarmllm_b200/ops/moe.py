@@ -5,7 +5,8 @@ One MoE layer is six launches, all sized from host-side bounds so the whole
 layer can be captured in a CUDA graph (the per-expert token counts stay on
 the device):
 
-    moe_route    router GEMV + bias + top-k + routing weights + expert counts
+    router GEMM  logits on the dense tensor-core GEMM (fp16 router weights)
+    moe_topk     bias + top-k + routing weights + expert counts
     moe_plan     per-expert offsets and the (expert, token-tile) tile list
     moe_scatter  token rows -> expert-sorted rows (fp16 for Q4_K experts,
                  bf16 for MXFP4 experts), destination slot per row
@@ -122,18 +123,23 @@ class MoeWorkspace:
             raise RuntimeError(f"MoE tile list overflow: {s[6]} tiles")
 
 
-def moe_ffn(x: torch.Tensor, experts: MoeExperts, router_w: torch.Tensor, router_type: int,
-            router_b: torch.Tensor | None, ws: MoeWorkspace, residual: torch.Tensor,
-            norm_w: torch.Tensor | None, out: torch.Tensor | None, eps: float,
-            softmax_after_topk: bool = True, shared=None, shared_gate=None):
-    """residual += MoE(x) (+ shared); out = RMSNorm(residual) * norm_w when out
-    is given.  x: fp16 [T, H] normed activations."""
+def moe_route(x: torch.Tensor, router, router_b: torch.Tensor | None, ws: MoeWorkspace,
+              gemm, softmax_after_topk: bool = True):
+    """Router logits (QLinear on `gemm`) -> top-k ids / weights / counts in ws."""
+    T = x.shape[0]
+    lg = router(x, gemm)
+    C().moe_topk(lg, router_b, T, ws.E, ws.k, softmax_after_topk, ws.ids, ws.wts, ws.counts)
+
+
+def moe_experts(x: torch.Tensor, experts: MoeExperts, ws: MoeWorkspace, residual: torch.Tensor,
+                norm_w: torch.Tensor | None, out: torch.Tensor | None, eps: float, shared=None,
+                shared_gate=None):
+    """Dispatch the routed rows, run the experts, combine into the residual
+    (+ shared expert); out = RMSNorm(residual) * norm_w when out is given."""
     T = x.shape[0]
     E, k = ws.E, ws.k
     P = T * k
     c = C()
-    c.moe_route(x, router_w, router_type, router_b, E, k, softmax_after_topk, ws.ids, ws.wts,
-                ws.counts)
     N = int(c.moe_tok_tile(P, E))
     c.moe_plan(ws.counts, E, N, ws.offsets, ws.cursor, ws.tiles, ws.n_tiles, ws.status)
     c.moe_scatter(x, ws.ids[:P], k, ws.cursor, ws.xs, ws.ret, 0)
@@ -145,3 +151,10 @@ def moe_ffn(x: torch.Tensor, experts: MoeExperts, router_w: torch.Tensor, router
                ex.b_down, ex.H, None, 0, 0.0, 0.0, [ws.rows.data_ptr()], ex.H, ws.ret,
                ws.num_sms, ws.status)
     c.moe_combine(ws.rows, ws.wts, k, shared, shared_gate, residual, norm_w, out, eps)
+
+
+def moe_ffn(x, experts, router, router_b, ws, gemm, residual, norm_w, out, eps,
+            softmax_after_topk: bool = True, shared=None, shared_gate=None):
+    """Routing + experts + combine in one call (no shared expert between)."""
+    moe_route(x, router, router_b, ws, gemm, softmax_after_topk)
+    moe_experts(x, experts, ws, residual, norm_w, out, eps, shared, shared_gate)

@@ -306,6 +306,23 @@ def test_paged_attention_tree_mask():
 
 
 # ----------------------------------------------------------------------------- sampling
+@pytest.mark.parametrize("rows,V", [(1, 201088), (3, 151936), (300, 9000), (2, 5000)])
+def test_argmax_split_paths(rows, V):
+    """Split (atomic 64-bit key) and single-CTA argmax: values, ties -> lowest
+    index, all-negative rows, and back-to-back calls (keys reset)."""
+    torch.manual_seed(rows)
+    logits = -torch.rand(rows, V) * 5 - 1          # all negative
+    logits[0, V // 3] = 2.0
+    logits[0, V - 7] = 2.0                         # tie: lower index wins
+    for _ in range(2):
+        out = torch.empty(rows, dtype=torch.int32, device=DEV)
+        val = torch.empty(rows, dtype=torch.float32, device=DEV)
+        C().argmax(logits.to(DEV), out, val)
+        torch.cuda.synchronize()
+        assert torch.equal(out.cpu().long(), logits.argmax(-1))
+        assert torch.equal(val.cpu(), logits.max(-1).values)
+
+
 def test_argmax_and_sampling():
     from swarmllm_b200.engine.sampling import SamplingParams, sample_host
     torch.manual_seed(0)

@@ -150,15 +150,15 @@ def test_hybrid_model_matches_cpu_oracle():
     src = RandomSource(cfg, seed=5)
     gpu = LlamaGPU(cfg, src, DEV)
     cpu = LlamaCPU(cfg, src)
-    ctx = gpu.make_context(64, 40, 256)
+    ctx = gpu.make_context(128, 128, 256)
     spec = gpu.linear_state_spec()
-    kvg = PagedKVCache(gpu.n_kv_layers, 8, cfg.n_kv_heads, cfg.head_dim, DEV)
-    kvc = PagedKVCache(cpu.n_kv_layers, 8, cfg.n_kv_heads, cfg.head_dim, "cpu", dtype=torch.float32)
+    kvg = PagedKVCache(gpu.n_kv_layers, 16, cfg.n_kv_heads, cfg.head_dim, DEV)
+    kvc = PagedKVCache(cpu.n_kv_layers, 16, cfg.n_kv_heads, cfg.head_dim, "cpu", dtype=torch.float32)
     kvg.add_linear_state(spec[0], 3, *spec[1:])
     kvc.add_linear_state(spec[0], 3, *spec[1:])
     rng = np.random.default_rng(1)
-    toks = rng.integers(0, cfg.vocab, 43)
-    bt = np.tile(np.arange(8, dtype=np.int32), (64, 1))
+    toks = rng.integers(0, cfg.vocab, 200)
+    bt = np.tile(np.arange(16, dtype=np.int32), (160, 1))
 
     def run(lo, hi):
         pos = np.arange(lo, hi)
@@ -167,10 +167,12 @@ def test_hybrid_model_matches_cpu_oracle():
         for dev, model, kv in ((DEV, gpu, kvg), ("cpu", cpu, kvc)):
             b = _batch(toks[lo:hi], pos, pos, bt[:hi - lo], dev, rows)
             b.ssm_seqs = torch.tensor([[0, hi - lo, 1, lo]], dtype=torch.int32, device=dev)
+            b.ssm_max_rows = hi - lo
             outs.append(model.forward(b, kv, ctx if dev == DEV else None))
         return torch.nn.functional.cosine_similarity(outs[0].cpu().double(), outs[1].double(), dim=-1)
 
-    for lo, hi in ((0, 24), (24, 40), (40, 41), (41, 42), (42, 43)):
+    # recurrent (<= 32 rows) and chunked (> 32 rows, partial chunks) paths, state handed over
+    for lo, hi in ((0, 24), (24, 40), (40, 41), (41, 141), (141, 142), (142, 143)):
         cos = run(lo, hi)
         assert float(cos.median()) > 0.999 and float(cos.min()) > 0.98, (lo, hi, cos)
     ctx.gemm.check()

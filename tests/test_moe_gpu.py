@@ -68,12 +68,17 @@ def test_moe_ffn_matches_oracle(fmt, E, k, H, F, T, after, bias):
                     act_kind=act_kind, alpha=alpha, limit=limit)
     wr = torch.from_numpy(rng.standard_normal((E, H), dtype=np.float32) * 0.1)
     br = torch.from_numpy(rng.standard_normal(E, dtype=np.float32) * 0.1) if bias else None
-    ws = MoeWorkspace(DEV, max(T, 8), H, F, E, k, ex.x_dtype, torch.cuda.get_device_properties(0).multi_processor_count)
+    nsm = torch.cuda.get_device_properties(0).multi_processor_count
+    ws = MoeWorkspace(DEV, max(T, 8), H, F, E, k, ex.x_dtype, nsm)
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    router = QLinear(torch.from_numpy(Q.quantize(wr.numpy(), Q.F32)), Q.F32, E, H, DEV, f32_as_f16=True)
+    gws = GemmWorkspace(DEV, max(T, 8), E)
+    wr = wr.half().float()  # the router runs with fp16 weights
     x = torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32)).half()
     resid0 = torch.from_numpy(rng.standard_normal((T, H), dtype=np.float32))
     for rep in range(2):  # second call reuses the zeroed counters
         resid = resid0.clone().to(DEV)
-        moe_ffn(x.to(DEV), ex, wr.to(DEV), Q.F32, br.to(DEV) if br is not None else None, ws,
+        moe_ffn(x.to(DEV), ex, router, br.to(DEV) if br is not None else None, ws, gws,
                 resid, None, None, 1e-5, softmax_after_topk=after)
         torch.cuda.synchronize()
         ws.check()
