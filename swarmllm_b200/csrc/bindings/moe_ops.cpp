@@ -47,7 +47,8 @@ void moe_scatter(Tensor x, Tensor ids, int64_t k, Tensor cursor, Tensor xs, Tens
 void moe_gemm(int64_t fmt, int64_t epi, Tensor w, int64_t rows, int64_t K, Tensor xs,
               int64_t tok_tile, Tensor tiles, Tensor n_tiles, OptT bias, int64_t bias_stride,
               OptT h, int64_t act_kind, double alpha, double limit, std::vector<int64_t> out_ptrs,
-              int64_t out_stride, OptT ret, int64_t num_sms, Tensor status) {
+              int64_t out_stride, OptT ret, int64_t num_sms, Tensor status, OptT sig_ctl,
+              std::vector<int64_t> sig_bases, int64_t sig_flag_off, int64_t sig_rank) {
   CHECK_CUDA(w); CHECK_CUDA(xs); CHECK_DT(tiles, at::kInt); CHECK_DT(status, at::kInt);
   TORCH_CHECK(status.numel() >= 8, "status must hold 8 ints");
   TORCH_CHECK(xs.scalar_type() == (fmt == 1 ? at::kBFloat16 : at::kHalf),
@@ -60,13 +61,18 @@ void moe_gemm(int64_t fmt, int64_t epi, Tensor w, int64_t rows, int64_t K, Tenso
   const at::cuda::CUDAGuard guard(xs.device());
   unsigned long long ptrs[8] = {0};
   for (size_t i = 0; i < out_ptrs.size() && i < 8; ++i) ptrs[i] = (unsigned long long)out_ptrs[i];
+  TORCH_CHECK(sig_bases.size() <= 8, "at most 8 ranks");
+  unsigned long long sb[8] = {0};
+  for (size_t i = 0; i < sig_bases.size(); ++i) sb[i] = (unsigned long long)sig_bases[i];
   int rc = launch_moe_gemm_tc(
       (int)fmt, (int)epi, w.data_ptr(), (int)rows, (int)K, xs.data_ptr(), (int)xs.stride(0),
       (int)xs.size(0), (int)tok_tile, tiles.data_ptr(), n_tiles.data_ptr<int>(),
       (int)tiles.size(0), ptr_or_null<float>(bias), (int)bias_stride, ptr_or_null<void>(h),
       h.has_value() ? (int)h->stride(0) : 0, (int)act_kind, (float)alpha, (float)limit, ptrs,
       (int)out_ptrs.size(), (int)out_stride, ptr_or_null<int32_t>(ret),
-      num_sms > 0 ? (int)num_sms : num_sms_of(xs), status.data_ptr<int>(), cur_stream());
+      num_sms > 0 ? (int)num_sms : num_sms_of(xs), status.data_ptr<int>(), cur_stream(),
+      ptr_or_null<int>(sig_ctl), sb, (long long)sig_flag_off, (int)sig_bases.size(),
+      (int)sig_rank);
   TORCH_CHECK(rc == 0, "moe_gemm failed: rc=", rc);
 }
 
@@ -103,7 +109,9 @@ void register_moe_ops(py::module& m) {
         py::arg("K"), py::arg("xs"), py::arg("tok_tile"), py::arg("tiles"), py::arg("n_tiles"),
         py::arg("bias"), py::arg("bias_stride"), py::arg("h"), py::arg("act_kind"),
         py::arg("alpha"), py::arg("limit"), py::arg("out_ptrs"), py::arg("out_stride"),
-        py::arg("ret"), py::arg("num_sms"), py::arg("status"));
+        py::arg("ret"), py::arg("num_sms"), py::arg("status"), py::arg("sig_ctl") = py::none(),
+        py::arg("sig_bases") = std::vector<int64_t>{}, py::arg("sig_flag_off") = 0,
+        py::arg("sig_rank") = 0);
   m.def("moe_combine", &moe_combine, py::arg("rows"), py::arg("wts"), py::arg("k"),
         py::arg("sh").none(true), py::arg("shg").none(true), py::arg("residual"),
         py::arg("norm_w"), py::arg("out"), py::arg("eps"));

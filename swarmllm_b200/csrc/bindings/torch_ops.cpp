@@ -249,6 +249,7 @@ static void segv_handler(int sig) {
 }
 
 void register_moe_ops(py::module& m);
+void register_ep_ops(py::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "swarmllm_b200 sm_100a kernels";
@@ -336,4 +337,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample);
   m.def("philox_uniform", &philox_uniform);
   register_moe_ops(m);
+  register_ep_ops(m);
 }

@@ -101,7 +101,9 @@ int launch_moe_gemm_tc(int fmt, int epi, const void* w, int rows, int K, const v
                        const int* n_tiles, int max_tiles, const float* bias, int bias_stride,
                        void* h, int h_stride, int act_kind, float alpha, float limit,
                        const unsigned long long* out_ptrs, int n_out, int out_stride,
-                       const int32_t* ret, int num_sms, int* status, cudaStream_t s);
+                       const int32_t* ret, int num_sms, int* status, cudaStream_t s,
+                       int* sig_ctl = nullptr, const unsigned long long* sig_bases = nullptr,
+                       long long sig_flag_off = 0, int sig_world = 0, int sig_rank = 0);
 int launch_moe_combine(const float* rows, int row_stride, const float* wts, int k,
                        const swarm::GemmOut* sh, const swarm::GemmOut* shg, float* residual,
                        int T, int H, const float* norm_w, __half* out, int out_stride, float eps,
@@ -121,3 +123,19 @@ int launch_delta_chunk(const float* qkv, int C, int nk, int nv, int D, const swa
                        const float* dt_bias, const float* A, const swarm::GemmOut& gz,
                        const float* norm_w, float eps, float* state, const void* seqs, int S,
                        int T, float* o_raw, __half* out, cudaStream_t s);
+
+// ---- expert parallelism over peer memory (ep_comm.cu) --------------------------
+long long ep_arena_bytes(int world, int cap, int H, int e_loc);
+void ep_arena_offsets(int world, int cap, int H, int e_loc, long long* out6);
+int ep_arena_alloc(long long bytes, void** ptr, void* handle64);
+int ep_arena_open(const void* handle64, void** ptr);
+int ep_arena_close(void* ptr, int own);
+int launch_ep_dispatch(const __half* x, int x_stride, int H, const int32_t* ids, int P, int k,
+                       int* counts, int E, int e_loc, int cap, int* cursor,
+                       const unsigned long long* bases, int world, int rank, int x_bf16,
+                       int* ctl, cudaStream_t s);
+int launch_ep_wait(unsigned long long own_base, int world, int cap, int H, int e_loc, int which,
+                   int* ctl, int* status, cudaStream_t s);
+int launch_ep_plan_owner(unsigned long long own_base, int world, int cap, int H, int e_loc,
+                         int tok_tile, void* tiles, int* n_tiles, int max_tiles, int* status,
+                         cudaStream_t s);

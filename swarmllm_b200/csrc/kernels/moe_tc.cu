@@ -30,6 +30,7 @@
 #include "qgemm_common.cuh"
 #include "quant_blocks.cuh"
 #include "tc_utils.cuh"
+#include "ep_common.cuh"
 
 #include <type_traits>
 
@@ -219,6 +220,12 @@ struct MoeGemmArgs {
   int out_stride;
   const int32_t* ret;
   int* status;
+  // optional completion signal to the peers (expert parallelism): ctl[0..1]
+  // = done counter, epoch; flag word at sig_bases[o] + sig_flag_off + 4 * rank
+  int* sig_ctl;
+  unsigned long long sig_bases[8];
+  long long sig_flag_off;
+  int sig_world, sig_rank;
 };
 
 SW_DEVICE float moe_act(float g, float u, int kind, float alpha, float limit) {
@@ -474,6 +481,8 @@ __global__ void __launch_bounds__(MCfg<N, FMT>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }
+  if (a.sig_ctl != nullptr)
+    ep_grid_done_signal(a.sig_ctl, a.sig_bases, a.sig_flag_off, a.sig_world, a.sig_rank);
 }
 
 // ============================================================== combine
@@ -642,7 +651,9 @@ int launch_moe_gemm_tc(int fmt, int epi, const void* w, int rows, int K, const v
                        const int* n_tiles, int max_tiles, const float* bias, int bias_stride,
                        void* h, int h_stride, int act_kind, float alpha, float limit,
                        const unsigned long long* out_ptrs, int n_out, int out_stride,
-                       const int32_t* ret, int num_sms, int* status, cudaStream_t s) {
+                       const int32_t* ret, int num_sms, int* status, cudaStream_t s,
+                       int* sig_ctl, const unsigned long long* sig_bases, long long sig_flag_off,
+                       int sig_world, int sig_rank) {
   if (fmt == kMoeFmtQ4K && K % 256) return -1;
   if (fmt == kMoeFmtMX && K % 64) return -1;  // TMA boxes + the bf16 pair layout
   if (epi == kMoeEpiSwiglu && (rows % 128)) return -1;  // 64 features (gate + up) per tile
@@ -673,11 +684,22 @@ int launch_moe_gemm_tc(int fmt, int epi, const void* w, int rows, int K, const v
   a.out_stride = out_stride;
   a.ret = ret;
   a.status = status;
+  a.sig_ctl = sig_ctl;
+  if (sig_ctl) {
+    if (sig_world > 8) return -1;
+    for (int i = 0; i < sig_world; ++i) a.sig_bases[i] = sig_bases[i];
+    a.sig_flag_off = sig_flag_off;
+    a.sig_world = sig_world;
+    a.sig_rank = sig_rank;
+  }
   CUtensorMap map;
   if (make_tmap_2d_16bit(&map, xs, xs_rows, K, xs_stride, tok_tile, 64, 128) != 0) return -2;
   const long long items = (long long)max_tiles * a.row_tiles;
-  const int ctas = (int)(items < num_sms ? items : num_sms);
-  if (ctas <= 0) return 0;
+  int ctas = (int)(items < num_sms ? items : num_sms);
+  if (ctas <= 0) {
+    if (!sig_ctl) return 0;
+    ctas = 1;  // the peers wait for the completion signal even when there is no work
+  }
   if (fmt == kMoeFmtQ4K)
     return epi == kMoeEpiSwiglu ? moe_launch_fmt<kMoeFmtQ4K, kMoeEpiSwiglu>(tok_tile, map, a, ctas, s)
                                 : moe_launch_fmt<kMoeFmtQ4K, kMoeEpiStore>(tok_tile, map, a, ctas, s);

@@ -96,7 +96,9 @@ class LLMEngine:
     # ------------------------------------------------------------------ construction
     @classmethod
     def from_config(cls, cfg: ModelConfig, device="cuda:0", ecfg: EngineConfig | None = None,
-                    source=None, seed: int = 0):
+                    source=None, seed: int = 0, ep=None):
+        """`ep`: expert-parallel group (parallel/ep.py) for MoE models served
+        with the experts split over the GPUs of a node."""
         from ..models.llama import LlamaCPU, LlamaGPU
         from ..models.weights import RandomSource
         ecfg = ecfg or EngineConfig()
@@ -104,7 +106,7 @@ class LLMEngine:
         if source is None:
             source = RandomSource(cfg, seed=seed, on_device=dev.type == "cuda")
         if dev.type == "cuda":
-            model = LlamaGPU(cfg, source, dev)
+            model = LlamaGPU(cfg, source, dev, ep=ep)
         else:
             model = LlamaCPU(cfg, source)
         return cls(model, cfg, ecfg, dev)

@@ -28,7 +28,7 @@ import torch
 from ..gguf import quants as Q
 from ..ops.attention import AttentionWorkspace, PagedKVCache, paged_attention
 from ..ops.linear import GemmWorkspace, QLinear
-from ..ops.moe import MoeExperts, MoeWorkspace, moe_experts, moe_route
+from ..ops.moe import MoeExperts, MoeWorkspace, moe_experts, moe_experts_ep, moe_route
 from ..utils.ext import C
 from .config import ModelConfig, rope_inv_freq
 
@@ -62,8 +62,12 @@ class _GpuLayer:
 
 class LlamaGPU:
     def __init__(self, cfg: ModelConfig, source, device, layer_range: tuple[int, int] | None = None,
-                 kv_layer_offset: int | None = None):
+                 kv_layer_offset: int | None = None, ep=None):
+        """`ep`: an EpGroup (parallel/ep.py) -- this rank then holds only its
+        share of every MoE layer's experts and exchanges tokens with the
+        other ranks inside each MoE layer."""
         self.cfg = cfg
+        self.ep = ep
         self.device = torch.device(device)
         lo, hi = layer_range or (0, cfg.n_layers)
         self.lo, self.hi = lo, hi
@@ -175,8 +179,10 @@ class LlamaGPU:
             biases = dict(gate_b=small(b + "ffn_gate_exps.bias").cpu(),
                           up_b=small(b + "ffn_up_exps.bias").cpu(),
                           down_b=small(b + "ffn_down_exps.bias").cpu())
+        ep = self.ep
+        shard = dict(e0=ep.rank * (E // ep.world), n_local=E // ep.world) if ep else {}
         L.experts = MoeExperts(g[0].view(E, F, rb_h), u[0].view(E, F, rb_h),
-                               d[0].view(E, H, rb_f), qt, H, F, dev,
+                               d[0].view(E, H, rb_f), qt, H, F, dev, **shard,
                                act_kind=1 if cfg.swiglu_limit else 0, alpha=cfg.swiglu_alpha,
                                limit=cfg.swiglu_limit, **biases)
         del g, u, d
@@ -309,7 +315,11 @@ class LlamaGPU:
                     C().epi_swiglu(g, None, S, 0, False, 0.0, 0.0, ctx.act_sh[:N])
                     shg = L.sh_gate(x, ctx.gemm_side)
                     sh = L.sh_down(ctx.act_sh[:N], ctx.gemm)
-                moe_experts(x, L.experts, ctx.moe, h, nxt_w, nxt_out, cfg.rms_eps, sh, shg)
+                if self.ep is not None:
+                    moe_experts_ep(x, L.experts, ctx.moe, self.ep, h, nxt_w, nxt_out, cfg.rms_eps,
+                                   sh, shg)
+                else:
+                    moe_experts(x, L.experts, ctx.moe, h, nxt_w, nxt_out, cfg.rms_eps, sh, shg)
                 continue
             g = L.wgu(x, ctx.gemm)
             C().epi_swiglu(g, None, cfg.ffn, 0, False, 0.0, 0.0, act)
@@ -362,7 +372,8 @@ class GpuForwardContext:
         if cfg.n_experts:
             ex = next(L.experts for L in model.layers if L.experts is not None)
             self.moe = MoeWorkspace(dev, max_tokens, H, cfg.expert_ffn, cfg.n_experts,
-                                    cfg.n_experts_used, ex.x_dtype, self.gemm.num_sms)
+                                    cfg.n_experts_used, ex.x_dtype, self.gemm.num_sms,
+                                    ep=model.ep)
             S = max(cfg.shared_expert_ffn, 1)
             self.act_sh = torch.zeros(max_tokens, S, dtype=torch.float16, device=dev)
         # Size the CUDA-core GEMM scratch up front (graph capture cannot grow it).

@@ -94,7 +94,7 @@ class MoeWorkspace:
     """Routing and dispatch buffers for up to `max_tokens` tokens."""
 
     def __init__(self, dev, max_tokens: int, H: int, F: int, E: int, k: int, x_dtype,
-                 num_sms: int, max_pairs: int | None = None):
+                 num_sms: int, max_pairs: int | None = None, ep=None):
         self.E, self.k, self.H, self.F = E, k, H, F
         P = max_pairs or max_tokens * k
         self.P = P
@@ -113,6 +113,12 @@ class MoeWorkspace:
         self.rows = torch.zeros(max_tokens * k, H, dtype=torch.float32, device=dev)
         self.status = torch.zeros(8, **i32)
         self.num_sms = num_sms
+        if ep is not None:  # owner side: rows from every rank
+            ep.setup(P, H, E, x_dtype)
+            rows = ep.world * P
+            self.ep_tiles = torch.zeros(int(C().moe_max_tiles(rows, ep.world * ep.e_loc, 16)),
+                                        4, **i32)
+            self.ep_h = torch.zeros(rows, F, dtype=x_dtype, device=dev)
 
     def check(self):
         s = self.status.cpu().tolist()
@@ -151,6 +157,34 @@ def moe_experts(x: torch.Tensor, experts: MoeExperts, ws: MoeWorkspace, residual
                ex.b_down, ex.H, None, 0, 0.0, 0.0, [ws.rows.data_ptr()], ex.H, ws.ret,
                ws.num_sms, ws.status)
     c.moe_combine(ws.rows, ws.wts, k, shared, shared_gate, residual, norm_w, out, eps)
+
+
+def moe_experts_ep(x: torch.Tensor, experts: MoeExperts, ws: "MoeWorkspace", ep,
+                   residual: torch.Tensor, norm_w: torch.Tensor | None, out: torch.Tensor | None,
+                   eps: float, shared=None, shared_gate=None):
+    """moe_experts with the experts split over the ranks of `ep`
+    (parallel/ep.py): P2P dispatch, grouped GEMMs on this rank's experts over
+    every rank's rows, P2P combine from the down-projection epilogue."""
+    T = x.shape[0]
+    k = ws.k
+    P = T * k
+    c = C()
+    ex = experts
+    c.ep_dispatch(x, ws.ids[:P], k, ws.counts, ws.E, ep.e_loc, ep.cap, ws.cursor, ep.bases,
+                  ep.rank, ep.x_bf16, ep.ctl)
+    c.ep_wait(ep.base, ep.world, ep.cap, ep.H, ep.e_loc, 0, ep.ctl, ws.status)
+    N = int(c.moe_tok_tile(P * ep.world, ep.e_loc))
+    c.ep_plan_owner(ep.base, ep.world, ep.cap, ep.H, ep.e_loc, N, ws.ep_tiles, ws.n_tiles,
+                    ws.status)
+    c.moe_gemm(ex.fmt, EPI_SWIGLU, ex.w_gu, 2 * ex.F, ex.H, ep.recv_x, N, ws.ep_tiles, ws.n_tiles,
+               ex.b_gu, 2 * ex.F, ws.ep_h, ex.act_kind, ex.alpha, ex.limit, [], 0, None,
+               ws.num_sms, ws.status)
+    c.moe_gemm(ex.fmt, EPI_STORE, ex.w_down, ex.H, ex.F, ws.ep_h, N, ws.ep_tiles, ws.n_tiles,
+               ex.b_down, ex.H, None, 0, 0.0, 0.0, ep.comb_ptrs, ex.H, ep.recv_ret, ws.num_sms,
+               ws.status, sig_ctl=ep.ctl[3:], sig_bases=ep.bases,
+               sig_flag_off=ep.off["flags_c"], sig_rank=ep.rank)
+    c.ep_wait(ep.base, ep.world, ep.cap, ep.H, ep.e_loc, 1, ep.ctl, ws.status)
+    c.moe_combine(ep.comb, ws.wts, k, shared, shared_gate, residual, norm_w, out, eps)
 
 
 def moe_ffn(x, experts, router, router_b, ws, gemm, residual, norm_w, out, eps,
