@@ -224,6 +224,10 @@ def main():
         return reference_arm(args)
     if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
         return single_gpu(args)
+    from swarmllm_b200.models.config import preset
+    if preset(args.model).n_experts:
+        from swarmllm_b200.parallel.bench_ep import ep_bench
+        return ep_bench(args)
     from swarmllm_b200.parallel.bench_pp import pipeline_bench
     return pipeline_bench(args)
 

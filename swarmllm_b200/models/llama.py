@@ -253,7 +253,9 @@ class LlamaGPU:
             else:
                 n += 6 + (1 if L.gated else 0)  # qkv GEMM, rope/KV, attention + combine, o GEMM, residual+norm
             if L.experts is not None:
-                n += 6 + (4 if L.sh_gu is not None else 0)
+                # router GEMM + top-k, then plan/scatter/2 grouped GEMMs/combine, or under
+                # expert parallelism send-counts/dispatch/wait/plan/2 GEMMs/wait/combine
+                n += 2 + (8 if self.ep is not None else 5) + (4 if L.sh_gu is not None else 0)
             else:
                 n += 4   # gate|up GEMM, SwiGLU, down GEMM, residual+norm
         if self.last:
