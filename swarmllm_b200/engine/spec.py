@@ -1,0 +1,246 @@
+"""Tree speculative decoding (greedy): a small drafter grows a token tree, the
+target model verifies every node in one forward, the longest path the target
+agrees with is kept.
+
+One round for a batch of sequences:
+  1. drafter: rows = its pending tokens (committed last round but not yet in
+     the drafter's KV) ending with the root (the last committed token); its
+     top-`width` tokens at the root start the tree
+  2. drafter, levels 1..depth-1: one row per frontier node, visibility = the
+     node's ancestors (tree attention mask), top-`width` children per node,
+     the `width` best by cumulative log-probability survive (DraftTree.expand)
+  3. target: one row per tree node (1 + depth*width rows per sequence), each
+     seeing the context plus its ancestors; greedy token per node
+  4. walk: from the root, follow the child carrying the target's token; the
+     path plus the target's token at its end (the bonus) are committed
+  5. both KV caches move the accepted nodes' rows to consecutive positions
+     (PagedKVCache.copy_slots) and drop the rest (BlockManager.truncate)
+
+Node i of a tree sits at logical KV index root + i (nodes are appended level
+by level in index order), so the DraftTree ancestor bitmask is directly the
+attention mask relative to tree_start = root.
+
+Greedy output equals the target's own greedy decoding: every committed token
+is the target's argmax given exactly the committed prefix.  With a drafter
+that agrees with the target, each round commits depth + 1 tokens for one
+target forward.
+
+Reference: the tree path of the reference's speculative executor (draft trees
+with a visibility bitmask, src/inference/draft_tree.rs:92,617; verify walk,
+src/inference/sampling.rs:496; KV rollback on rejection).
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from ..models.llama import StepBatch
+from ..ops.attention import PagedKVCache
+from ..utils.ext import native
+
+
+@dataclass
+class SpecStats:
+    rounds: int = 0
+    committed: int = 0
+    accepted: int = 0       # drafted tokens the target agreed with
+    seconds: float = 0.0
+
+    @property
+    def tokens_per_round(self) -> float:
+        return self.committed / max(1, self.rounds)
+
+
+@dataclass
+class _Seq:
+    sid: int
+    max_new: int
+    out: list = field(default_factory=list)
+    pos: int = 0            # tokens in the target KV
+    root: int = 0           # last committed token (in neither KV yet)
+    dpos: int = 0           # tokens in the drafter KV
+    pending: list = field(default_factory=list)  # committed, not yet in the drafter KV
+
+    @property
+    def done(self) -> bool:
+        return len(self.out) >= self.max_new
+
+
+class _Side:
+    """One model with its paged KV cache, block manager and forward context."""
+
+    def __init__(self, model, max_rows: int, max_samples: int, max_len: int, max_seqs: int,
+                 page: int = 16):
+        cfg = model.cfg
+        self.model = model
+        self.page = page
+        self.pages_per_seq = (max_len + page - 1) // page
+        pages = max_seqs * self.pages_per_seq + 1
+        self.kv = PagedKVCache(model.n_kv_layers, pages, cfg.n_kv_heads, cfg.head_dim,
+                               model.device, page)
+        self.bm = native().BlockManager(pages, page, False)
+        self.ctx = model.make_context(max_rows, max_samples, max_len)
+        self.max_len = max_len
+        self.dev = model.device
+
+    def phys(self, sid: int, logical) -> list[int]:
+        bt = self.bm.block_table([sid], self.pages_per_seq)[0]
+        return [int(bt[i // self.page]) * self.page + i % self.page for i in logical]
+
+    def forward(self, rows: list[tuple], sample_rows: list[int], tree: bool) -> torch.Tensor:
+        """rows: (sid, token, position, slot, seq_len, tree_start, mask)."""
+        d = self.dev
+        sids = sorted({r[0] for r in rows})
+        bt_seq = dict(zip(sids, self.bm.block_table(sids, self.pages_per_seq)))
+        t = lambda a, dt=torch.int32: torch.as_tensor(np.asarray(a), dtype=dt).to(d)
+        b = StepBatch(t([r[1] for r in rows]), t([r[2] for r in rows]), t([r[3] for r in rows]),
+                      t(np.stack([bt_seq[r[0]] for r in rows])), t([r[4] for r in rows]),
+                      t(sample_rows, torch.int64), self.max_len)
+        if tree:
+            b.tree_start = t([r[5] for r in rows])
+            b.tree_mask = t(np.asarray([r[6] for r in rows], dtype=np.uint64).view(np.int64),
+                            torch.int64)
+        return self.model.forward(b, self.kv, self.ctx)
+
+    def commit_path(self, sid: int, root: int, path: list[int], keep: int):
+        """Move nodes path[1:keep] (at logical root + node) to root + 1.. and
+        truncate the sequence after them."""
+        if keep > 1:
+            src = self.phys(sid, [root + n for n in path[1:keep]])
+            dst = self.phys(sid, [root + i for i in range(1, keep)])
+            if src != dst:
+                self.kv.copy_slots(torch.tensor(src, device=self.dev),
+                                   torch.tensor(dst, device=self.dev))
+        self.bm.truncate(sid, root + keep)
+
+
+class TreeSpecDecoder:
+    def __init__(self, target, drafter, depth: int = 4, width: int = 4, max_seqs: int = 32,
+                 max_model_len: int = 4096, prefill_chunk: int = 2048):
+        assert 1 + depth * width <= 64, "tree masks are 64-bit: at most 64 nodes"
+        assert target.cfg.vocab == drafter.cfg.vocab, "drafter and target share a vocabulary"
+        self.depth, self.width = depth, width
+        self.n_nodes = 1 + depth * width
+        self.chunk = prefill_chunk
+        ml = max_model_len + self.n_nodes + 16
+        self.t = _Side(target, max(prefill_chunk, max_seqs * self.n_nodes),
+                       max_seqs * self.n_nodes, ml, max_seqs)
+        self.d = _Side(drafter, max(prefill_chunk, max_seqs * (width + 2)), max_seqs * width,
+                       ml, max_seqs)
+        self.stats = SpecStats()
+        self._next_sid = 0
+
+    # ------------------------------------------------------------------ prefill
+    def _prefill(self, side: _Side, sid: int, prompt: list[int]) -> torch.Tensor:
+        side.bm.add_sequence(sid, prompt)
+        slots = list(side.bm.append_slots(sid, len(prompt)))
+        logits = None
+        for c0 in range(0, len(prompt), self.chunk):
+            c1 = min(len(prompt), c0 + self.chunk)
+            rows = [(sid, prompt[i], i, slots[i], i + 1, 0, 0) for i in range(c0, c1)]
+            logits = side.forward(rows, [c1 - c0 - 1], tree=False)
+        return logits
+
+    def add(self, prompt: list[int], max_new: int) -> _Seq:
+        sid = self._next_sid
+        self._next_sid += 1
+        s = _Seq(sid, max_new)
+        lg = self._prefill(self.t, sid, prompt)
+        self._prefill(self.d, sid, prompt)
+        s.root = int(lg[0].argmax())
+        s.out.append(s.root)
+        s.pos = s.dpos = len(prompt)
+        return s
+
+    # ------------------------------------------------------------------ one round
+    def _draft(self, seqs: list[_Seq]):
+        W, D = self.width, self.depth
+        rows, samp, roots = [], [], {}
+        for s in seqs:
+            toks = s.pending + [s.root]
+            slots = list(self.d.bm.append_slots(s.sid, len(toks)))
+            for j, tok in enumerate(toks):
+                p = s.dpos + j
+                rows.append((s.sid, tok, p, slots[j], p + 1, 0, 0))
+            samp.append(len(rows) - 1)
+            roots[s.sid] = s.dpos + len(toks) - 1
+        lp = torch.log_softmax(self.d.forward(rows, samp, tree=False).float(), -1)
+        v, ix = (a.cpu().numpy() for a in torch.topk(lp, W, dim=-1))
+        trees, fronts = {}, {}
+        for n, s in enumerate(seqs):
+            tr = native().DraftTree(s.root, self.n_nodes)
+            fronts[s.sid] = tr.expand(ix[n].tolist(), v[n].tolist(), W, W)
+            trees[s.sid] = tr
+        for _ in range(1, D):
+            rows = []
+            for s in seqs:
+                tr, fr, r = trees[s.sid], fronts[s.sid], roots[s.sid]
+                slots = list(self.d.bm.append_slots(s.sid, len(fr)))
+                masks, toks, deps = tr.masks(), tr.tokens(), tr.depths()
+                for j, node in enumerate(fr):
+                    rows.append((s.sid, toks[node], r + deps[node], slots[j], r + len(tr), r,
+                                 int(masks[node])))
+            lp = torch.log_softmax(self.d.forward(rows, list(range(len(rows))), tree=True).float(), -1)
+            v, ix = (a.cpu().numpy() for a in torch.topk(lp, W, dim=-1))
+            k0 = 0
+            for s in seqs:
+                tr, nf = trees[s.sid], len(fronts[s.sid])
+                fronts[s.sid] = tr.expand(ix[k0:k0 + nf].reshape(-1).tolist(),
+                                          v[k0:k0 + nf].reshape(-1).tolist(), W, W)
+                k0 += nf
+        return trees, roots
+
+    def step(self, seqs: list[_Seq]):
+        seqs = [s for s in seqs if not s.done]
+        if not seqs:
+            return
+        t0 = time.perf_counter()
+        trees, droots = self._draft(seqs)
+        # ---- verify every node with the target
+        rows = []
+        for s in seqs:
+            tr = trees[s.sid]
+            n = len(tr)
+            slots = list(self.t.bm.append_slots(s.sid, n))
+            masks, toks, deps = tr.masks(), tr.tokens(), tr.depths()
+            for i in range(n):
+                rows.append((s.sid, toks[i], s.pos + deps[i], slots[i], s.pos + n, s.pos,
+                             int(masks[i])))
+        logits = self.t.forward(rows, list(range(len(rows))), tree=True)
+        tgt = logits.argmax(-1).cpu().numpy()
+        k0 = 0
+        for s in seqs:
+            tr = trees[s.sid]
+            n = len(tr)
+            path, bonus = tr.walk(tgt[k0:k0 + n].tolist())
+            k0 += n
+            toks = tr.tokens()
+            new = [toks[i] for i in path[1:]] + [bonus]
+            # target: root + accepted nodes now sit at pos .. pos + len(path) - 1
+            self.t.commit_path(s.sid, s.pos, path, len(path))
+            # drafter: nodes of depth < depth have drafter KV (the last level was never fed)
+            r = droots[s.sid]
+            keep = min(len(path), self.depth)
+            self.d.commit_path(s.sid, r, path, keep)
+            s.dpos = r + keep
+            s.pending = [toks[i] for i in path[keep:]]
+            s.pos += len(path)
+            s.root = bonus
+            room = s.max_new - len(s.out)
+            s.out.extend(new[:room])
+            self.stats.committed += min(len(new), room)
+            self.stats.accepted += len(path) - 1
+        self.stats.rounds += 1
+        self.stats.seconds += time.perf_counter() - t0
+
+    def generate(self, prompts: list[list[int]], max_new: int) -> list[list[int]]:
+        seqs = [self.add(p, max_new) for p in prompts]
+        while any(not s.done for s in seqs):
+            self.step(seqs)
+        for s in seqs:
+            self.t.bm.free_sequence(s.sid)
+            self.d.bm.free_sequence(s.sid)
+        return [s.out for s in seqs]
