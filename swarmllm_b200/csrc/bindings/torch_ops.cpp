@@ -292,6 +292,26 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                                   out.data_ptr<float>(), cur_stream());
     TORCH_CHECK(rc == 0, "ssm_conv_silu failed: rc=", rc);
   });
+  m.def("tree_rank", [](Tensor logits, int64_t k, Tensor ids, Tensor logp, Tensor ws) {
+    // ws: float32 scratch of at least rows * S * (2k + 2) elements (tree_rank_ws_floats)
+    CHECK_DT(logits, at::kFloat); CHECK_DT(ids, at::kInt); CHECK_DT(logp, at::kFloat);
+    CHECK_DT(ws, at::kFloat);
+    TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits [rows, V] row-major");
+    const int rows = (int)logits.size(0), V = (int)logits.size(1);
+    TORCH_CHECK(ids.numel() >= rows * k && logp.numel() >= rows * k, "outputs too small");
+    const int S = tree_rank_slices(rows, V);
+    TORCH_CHECK(ws.numel() >= (int64_t)rows * S * (2 * k + 2), "tree_rank workspace too small");
+    const at::cuda::CUDAGuard guard(logits.device());
+    float* base = ws.data_ptr<float>();
+    int rc = launch_tree_rank(logits.data_ptr<float>(), rows, V, (int)logits.stride(0), (int)k,
+                              base, reinterpret_cast<int*>(base + (size_t)rows * S * k),
+                              base + (size_t)rows * S * 2 * k, S, ids.data_ptr<int32_t>(),
+                              logp.data_ptr<float>(), cur_stream());
+    TORCH_CHECK(rc == 0, "tree_rank failed: rc=", rc);
+  });
+  m.def("tree_rank_ws_floats", [](int64_t rows, int64_t V, int64_t k) {
+    return (int64_t)rows * tree_rank_slices((int)rows, (int)V) * (2 * k + 2);
+  });
   m.def("delta_chunk", [](Tensor qkv, int64_t nk, int64_t nv, int64_t D, const GemmResult& gba,
                           Tensor dt_bias, Tensor A, const GemmResult& gz, Tensor norm_w, double eps,
                           Tensor state, Tensor seqs, int64_t S, Tensor o_raw, Tensor out) {

@@ -139,3 +139,8 @@ int launch_ep_wait(unsigned long long own_base, int world, int cap, int H, int e
 int launch_ep_plan_owner(unsigned long long own_base, int world, int cap, int H, int e_loc,
                          int tok_tile, void* tiles, int* n_tiles, int max_tiles, int* status,
                          cudaStream_t s);
+
+// ---- speculative tree ranking (tree_rank.cu) ---------------------------------
+int tree_rank_slices(int rows, int V);
+int launch_tree_rank(const float* logits, int rows, int V, int stride, int k, float* cand_v,
+                     int* cand_i, float* ms, int S, int32_t* ids, float* logp, cudaStream_t s);

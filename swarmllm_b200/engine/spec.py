@@ -5,7 +5,8 @@ agrees with is kept.
 One round for a batch of sequences:
   1. drafter: rows = its pending tokens (committed last round but not yet in
      the drafter's KV) ending with the root (the last committed token); its
-     top-`width` tokens at the root start the tree
+     top-`width` tokens at the root (tree_rank kernel: log-sum-exp + top-k on
+     the device) start the tree
   2. drafter, levels 1..depth-1: one row per frontier node, visibility = the
      node's ancestors (tree attention mask), top-`width` children per node,
      the `width` best by cumulative log-probability survive (DraftTree.expand)
@@ -39,7 +40,7 @@ import torch
 
 from ..models.llama import StepBatch
 from ..ops.attention import PagedKVCache
-from ..utils.ext import native
+from ..utils.ext import C, native
 
 
 @dataclass
@@ -132,6 +133,20 @@ class TreeSpecDecoder:
                        ml, max_seqs)
         self.stats = SpecStats()
         self._next_sid = 0
+        rows = max_seqs * width
+        V = drafter.cfg.vocab
+        dev = drafter.device
+        self._rk_ids = torch.zeros(rows * width, dtype=torch.int32, device=dev)
+        self._rk_lp = torch.zeros(rows * width, dtype=torch.float32, device=dev)
+        self._rk_ws = torch.zeros(int(C().tree_rank_ws_floats(rows, V, width)),
+                                  dtype=torch.float32, device=dev)
+
+    def _rank(self, logits: torch.Tensor):
+        """Top-`width` (log-prob, token) per row on the device (tree_rank kernel)."""
+        n, W = logits.shape[0], self.width
+        C().tree_rank(logits, W, self._rk_ids, self._rk_lp, self._rk_ws)
+        return (self._rk_lp[:n * W].view(n, W).cpu().numpy(),
+                self._rk_ids[:n * W].view(n, W).cpu().numpy())
 
     # ------------------------------------------------------------------ prefill
     def _prefill(self, side: _Side, sid: int, prompt: list[int]) -> torch.Tensor:
@@ -167,8 +182,7 @@ class TreeSpecDecoder:
                 rows.append((s.sid, tok, p, slots[j], p + 1, 0, 0))
             samp.append(len(rows) - 1)
             roots[s.sid] = s.dpos + len(toks) - 1
-        lp = torch.log_softmax(self.d.forward(rows, samp, tree=False).float(), -1)
-        v, ix = (a.cpu().numpy() for a in torch.topk(lp, W, dim=-1))
+        v, ix = self._rank(self.d.forward(rows, samp, tree=False))
         trees, fronts = {}, {}
         for n, s in enumerate(seqs):
             tr = native().DraftTree(s.root, self.n_nodes)
@@ -183,8 +197,7 @@ class TreeSpecDecoder:
                 for j, node in enumerate(fr):
                     rows.append((s.sid, toks[node], r + deps[node], slots[j], r + len(tr), r,
                                  int(masks[node])))
-            lp = torch.log_softmax(self.d.forward(rows, list(range(len(rows))), tree=True).float(), -1)
-            v, ix = (a.cpu().numpy() for a in torch.topk(lp, W, dim=-1))
+            v, ix = self._rank(self.d.forward(rows, list(range(len(rows))), tree=True))
             k0 = 0
             for s in seqs:
                 tr, nf = trees[s.sid], len(fronts[s.sid])

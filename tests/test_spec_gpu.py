@@ -59,3 +59,22 @@ def test_tree_spec_self_draft_accepts():
     ref = _greedy_reference(cfg, 7, prompts, 21)
     agree = np.mean([a == b for o, r in zip(out, ref) for a, b in zip(o, r)])
     assert agree >= 0.95, (agree, out, ref)
+
+
+@pytest.mark.parametrize("rows,V,k", [(1, 128256, 4), (4, 151936, 16), (300, 5000, 8), (7, 1000, 2)])
+def test_tree_rank_matches_torch(rows, V, k):
+    from swarmllm_b200.utils.ext import C
+    torch.manual_seed(rows + k)
+    logits = torch.randn(rows, V) * 4
+    logits[0, 17] = logits[0, 23] = 50.0  # tie: lower id first
+    ids = torch.zeros(rows * k, dtype=torch.int32, device=DEV)
+    lp = torch.zeros(rows * k, dtype=torch.float32, device=DEV)
+    ws = torch.zeros(int(C().tree_rank_ws_floats(rows, V, k)), dtype=torch.float32, device=DEV)
+    for _ in range(2):
+        C().tree_rank(logits.to(DEV), k, ids, lp, ws)
+        torch.cuda.synchronize()
+        ref_lp, ref_ix = torch.topk(torch.log_softmax(logits.double(), -1), k, dim=-1)
+        got = ids.view(rows, k).cpu().long()
+        assert torch.equal(got[1:], ref_ix[1:]) and torch.equal(got[0, 2:], ref_ix[0, 2:])
+        assert ids.view(rows, k)[0, 0].item() == 17 and ids.view(rows, k)[0, 1].item() == 23
+        assert torch.allclose(lp.view(rows, k).cpu().double(), ref_lp, atol=1e-4)
