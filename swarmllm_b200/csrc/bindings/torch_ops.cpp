@@ -140,6 +140,39 @@ py::tuple dense_tc_plan_py(int64_t rows, int64_t K, int64_t T, int64_t num_sms) 
   return py::make_tuple(N, ntt, kb, total, upc, ctas, need);
 }
 
+// Row-parallel Q4_K GEMM of a tensor-parallel group: partial tiles pushed to
+// every rank's receive buffer (dst_ptrs[o]); the result reads this rank's
+// receive buffer, summing the n ranks' partials (src_stride floats apart).
+GemmResult qgemm_q4k_tc_tp(Tensor w_packed, int64_t rows, int64_t K, Tensor x, Tensor status,
+                           int64_t num_sms, int64_t recv_base, int64_t src_stride,
+                           std::vector<int64_t> dst_ptrs, Tensor sig_ctl,
+                           std::vector<int64_t> sig_bases, int64_t sig_flag_off, int64_t rank) {
+  CHECK_CUDA(w_packed); CHECK_DT(x, at::kHalf); CHECK_DT(status, at::kInt);
+  CHECK_DT(sig_ctl, at::kInt);
+  TORCH_CHECK(x.size(-1) == K && x.stride(-1) == 1, "x must be [T, K] with unit inner stride");
+  TORCH_CHECK(dst_ptrs.size() == sig_bases.size() && !dst_ptrs.empty() && dst_ptrs.size() <= 8,
+              "1..8 ranks");
+  const at::cuda::CUDAGuard guard(x.device());
+  if (num_sms <= 0) num_sms = num_sms_of(x);
+  unsigned long long d[8], b[8];
+  for (size_t i = 0; i < dst_ptrs.size(); ++i) {
+    d[i] = (unsigned long long)dst_ptrs[i];
+    b[i] = (unsigned long long)sig_bases[i];
+  }
+  GemmResult r;
+  float* own = reinterpret_cast<float*>(recv_base);
+  int rc = launch_qgemm_q4k_tc(w_packed.data_ptr(), (int)rows, (int)K,
+                               reinterpret_cast<const __half*>(x.data_ptr()), (int)x.stride(0),
+                               (int)x.size(0), own, (size_t)src_stride, (int)num_sms,
+                               status.data_ptr<int>(), &r.g, cur_stream(), d,
+                               (int)dst_ptrs.size(), sig_ctl.data_ptr<int>(), b,
+                               (long long)sig_flag_off, (int)rank);
+  TORCH_CHECK(rc == 0, "qgemm_q4k_tc_tp launch failed: rc=", rc);
+  r.g.n_src = (int)dst_ptrs.size();
+  r.g.src_stride = src_stride;
+  return r;
+}
+
 void qgemm_set_trace_py(OptT buf) {
   if (buf.has_value()) TORCH_CHECK(buf->numel() * buf->element_size() >= 512 * 8 * 8, "trace buffer too small");
   qgemm_set_trace(ptr_or_null<void>(buf));
@@ -346,6 +379,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qmatmul_simt", &qmatmul_simt);
   m.def("q4k_tc_plan", &q4k_tc_plan_py);
   m.def("qgemm_q4k_tc", &qgemm_q4k_tc);
+  m.def("qgemm_q4k_tc_tp", &qgemm_q4k_tc_tp);
+  m.def("flag_wait", [](int64_t flags, int64_t world, Tensor ctl, int64_t slot, Tensor status,
+                        int64_t code) {
+    const at::cuda::CUDAGuard guard(ctl.device());
+    TORCH_CHECK(launch_flag_wait(reinterpret_cast<const void*>(flags), (int)world,
+                                 ctl.data_ptr<int>(), (int)slot, status.data_ptr<int>(), (int)code,
+                                 cur_stream()) == 0, "flag_wait launch failed");
+  });
   m.def("q4k_repack", &q4k_repack);
   m.def("dense_gemm_tc", &dense_gemm_tc);
   m.def("dense_tc_plan", &dense_tc_plan_py);

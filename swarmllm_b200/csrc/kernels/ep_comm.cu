@@ -275,3 +275,11 @@ int launch_ep_plan_owner(unsigned long long own_base, int world, int cap, int H,
       (int4*)tiles, n_tiles, max_tiles, status);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }
+
+int launch_flag_wait(const void* flags, int world, int* ctl, int slot, int* status, int code,
+                     cudaStream_t s) {
+  if (world < 1 || world > 32) return -1;
+  ep_wait_kernel<<<1, 32, 0, s>>>(reinterpret_cast<const uint32_t*>(flags), world, ctl, slot,
+                                  status, code);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}

@@ -11,6 +11,10 @@
 // [T, rows] result.
 //
 // mode 0 is a plain dense [T][rows] fp32 buffer (SIMT GEMM, tests).
+// n_src > 1: the partials of n_src ranks of a tensor-parallel group, pushed
+// into this rank's buffer by their GEMM epilogues, sit src_stride floats
+// apart; get() then also sums over the ranks (the all-reduce happens while
+// reading).
 // The struct is plain data so host C++ (the torch bindings) can hold it.
 #pragma once
 #include <stddef.h>
@@ -27,6 +31,8 @@ struct GemmOut {
   int tok_tile;   // tokens per token-tile (N of the MMA)
   int n_tok_tiles;
   int seg_max;    // unused; kept so the struct layout stays fixed
+  int n_src;      // ranks whose partials are summed (0 or 1: just this one)
+  long long src_stride;
 
 #ifdef __CUDACC__
   __device__ __forceinline__ float get(int t, int r) const {
@@ -38,7 +44,11 @@ struct GemmOut {
     const int c0 = (int)(u0 / upc);
     const int c1 = (int)((u0 + ksb - 1) / upc);
     float acc = 0.f;
-    for (int c = c0; c <= c1; ++c) acc += ws[((size_t)(tile + c) * tok_tile + tt) * 128 + rr];
+    const int ns = n_src > 1 ? n_src : 1;
+    for (int s = 0; s < ns; ++s) {
+      const float* w = ws + (size_t)s * src_stride;
+      for (int c = c0; c <= c1; ++c) acc += w[((size_t)(tile + c) * tok_tile + tt) * 128 + rr];
+    }
     return acc;
   }
 #endif

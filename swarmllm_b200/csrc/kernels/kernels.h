@@ -40,7 +40,10 @@ void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_
                  long* total_units, int* upc, int* n_ctas, size_t* ws_floats);
 int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, int x_stride,
                         int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
-                        swarm::GemmOut* out, cudaStream_t s);
+                        swarm::GemmOut* out, cudaStream_t s,
+                        const unsigned long long* peer_ws = nullptr, int n_peers = 0,
+                        int* sig_ctl = nullptr, const unsigned long long* sig_bases = nullptr,
+                        long long sig_flag_off = 0, int sig_rank = 0);
 void qgemm_set_trace(void* buf);
 // Dense fp16 weights on tcgen05 (dense_gemm_tc.cu); same workspace contract.
 void dense_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* kb,
@@ -144,3 +147,7 @@ int launch_ep_plan_owner(unsigned long long own_base, int world, int cap, int H,
 int tree_rank_slices(int rows, int V);
 int launch_tree_rank(const float* logits, int rows, int V, int stride, int k, float* cand_v,
                      int* cand_i, float* ms, int S, int32_t* ids, float* logp, cudaStream_t s);
+// Bounded wait (one CTA) until flags[0..world) reach this side's next epoch
+// (ctl[slot] + 1); records code/where in status on timeout.
+int launch_flag_wait(const void* flags, int world, int* ctl, int slot, int* status, int code,
+                     cudaStream_t s);

@@ -35,6 +35,7 @@
 #include "gemm_out.cuh"
 #include "qgemm_common.cuh"
 #include "tc_utils.cuh"
+#include "ep_common.cuh"
 
 namespace swarm {
 using namespace tc;
@@ -77,6 +78,15 @@ struct QGemmArgs {
   float* ws;
   int* status;
   unsigned long long* trace;  // debug: per-unit event timestamps of CTA 0 (null = off)
+  // Tensor parallelism: when n_peers > 0 the partial tiles go to every rank's
+  // receive buffer (peer_ws[o], over NVLink) instead of `ws`, and the CTA that
+  // finishes last raises flag word sig_bases[o] + sig_flag_off + 4 * sig_rank.
+  int n_peers;
+  unsigned long long peer_ws[8];
+  int* sig_ctl;
+  unsigned long long sig_bases[8];
+  long long sig_flag_off;
+  int sig_rank;
 };
 
 // Debug timeline of CTA 0 (see qgemm_set_trace): trace[unit*8 + event] = %globaltimer.
@@ -256,15 +266,26 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
           tc_fence_after();
           const int nt = tile % a.n_tok_tiles;
           const int n_valid = min(N, a.T - nt * N);
-          float* dst = a.ws + ((size_t)(tile + blockIdx.x) * N) * 128 + row;
+          const size_t off = ((size_t)(tile + blockIdx.x) * N) * 128 + row;
 #pragma unroll 1
           for (int c = 0; c < N / 16; ++c) {
             uint32_t r[16];
             tmem_ld_x16(tmem_base + lane_off + c * 16, r);
             tmem_wait_ld();
+            if (a.n_peers == 0) {
+              float* dst = a.ws + off;
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-              if (c * 16 + e < n_valid) dst[(size_t)(c * 16 + e) * 128] = __uint_as_float(r[e]);
+              for (int e = 0; e < 16; ++e)
+                if (c * 16 + e < n_valid) dst[(size_t)(c * 16 + e) * 128] = __uint_as_float(r[e]);
+            } else {
+              for (int o = 0; o < a.n_peers; ++o) {
+                float* dst = reinterpret_cast<float*>(a.peer_ws[o]) + off;
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                  if (c * 16 + e < n_valid)
+                    dst[(size_t)(c * 16 + e) * 128] = __uint_as_float(r[e]);
+              }
+            }
           }
           tc_fence_before();
           __syncwarp();
@@ -281,6 +302,8 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  if (a.sig_ctl != nullptr)
+    ep_grid_done_signal(a.sig_ctl, a.sig_bases, a.sig_flag_off, a.n_peers, a.sig_rank);
 }
 
 // GGUF Q4_K [rows][K/256 blocks] -> tiled, nibble-permuted layout
@@ -403,7 +426,9 @@ static int launch_n(const CUtensorMap& map, const QGemmArgs& a, int n_ctas, cuda
 
 int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, int x_stride,
                         int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
-                        GemmOut* out, cudaStream_t s) {
+                        GemmOut* out, cudaStream_t s, const unsigned long long* peer_ws,
+                        int n_peers, int* sig_ctl, const unsigned long long* sig_bases,
+                        long long sig_flag_off, int sig_rank) {
   if (T <= 0) return 0;
   if (K % 256 != 0 || rows % 128 != 0) return -1;
   if ((x_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return -5;
@@ -415,6 +440,19 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
   CUtensorMap map;
   if (make_tmap_2d_16bit(&map, x, T, K, x_stride, N, 64, 128) != 0) return -2;
   QGemmArgs a{(const uint8_t*)w_packed, rows, K, T, ntt, kb, total, upc, ws, status, g_trace};
+  a.n_peers = 0;
+  a.sig_ctl = nullptr;
+  if (n_peers > 0) {
+    if (n_peers > 8 || !peer_ws || !sig_ctl || !sig_bases) return -7;
+    a.n_peers = n_peers;
+    for (int i = 0; i < n_peers; ++i) {
+      a.peer_ws[i] = peer_ws[i];
+      a.sig_bases[i] = sig_bases[i];
+    }
+    a.sig_ctl = sig_ctl;
+    a.sig_flag_off = sig_flag_off;
+    a.sig_rank = sig_rank;
+  }
   int rc;
   switch (N) {
     case 16: rc = launch_n<16>(map, a, ctas, s); break;

@@ -66,8 +66,8 @@ class LLMEngine:
         if self.device.type == "cuda":
             pages = ecfg.kv_pages or self._auto_pages()
             # one extra page: the trash page that graph padding rows write to
-            self.kv = PagedKVCache(n_kv_layers, pages + 1, cfg.n_kv_heads, cfg.head_dim,
-                                   self.device, ps)
+            self.kv = PagedKVCache(n_kv_layers, pages + 1, getattr(model, "n_kv", cfg.n_kv_heads),
+                                   cfg.head_dim, self.device, ps)
             if lin is not None:
                 self.kv.add_linear_state(lin[0], max(ecfg.max_running, max(ecfg.graph_sizes)) + 1,
                                          *lin[1:])
@@ -96,7 +96,7 @@ class LLMEngine:
     # ------------------------------------------------------------------ construction
     @classmethod
     def from_config(cls, cfg: ModelConfig, device="cuda:0", ecfg: EngineConfig | None = None,
-                    source=None, seed: int = 0, ep=None):
+                    source=None, seed: int = 0, ep=None, tp=None):
         """`ep`: expert-parallel group (parallel/ep.py) for MoE models served
         with the experts split over the GPUs of a node."""
         from ..models.llama import LlamaCPU, LlamaGPU
@@ -106,7 +106,7 @@ class LLMEngine:
         if source is None:
             source = RandomSource(cfg, seed=seed, on_device=dev.type == "cuda")
         if dev.type == "cuda":
-            model = LlamaGPU(cfg, source, dev, ep=ep)
+            model = LlamaGPU(cfg, source, dev, ep=ep, tp=tp)
         else:
             model = LlamaCPU(cfg, source)
         return cls(model, cfg, ecfg, dev)
@@ -121,7 +121,7 @@ class LLMEngine:
         free, _ = torch.cuda.mem_get_info(self.device)
         per_page = PagedKVCache.bytes_per_page(getattr(self.model, "n_kv_layers",
                                                        self.model.hi - self.model.lo),
-                                               self.cfg.n_kv_heads,
+                                               getattr(self.model, "n_kv", self.cfg.n_kv_heads),
                                                self.cfg.head_dim, self.ecfg.page_size)
         # leave room for activations / workspaces
         budget = free * self.ecfg.kv_fraction - 4 * (1 << 30)

@@ -80,7 +80,7 @@ class _Side:
         self.page = page
         self.pages_per_seq = (max_len + page - 1) // page
         pages = max_seqs * self.pages_per_seq + 1
-        self.kv = PagedKVCache(model.n_kv_layers, pages, cfg.n_kv_heads, cfg.head_dim,
+        self.kv = PagedKVCache(model.n_kv_layers, pages, model.n_kv, cfg.head_dim,
                                model.device, page)
         self.bm = native().BlockManager(pages, page, False)
         self.ctx = model.make_context(max_rows, max_samples, max_len)

@@ -28,6 +28,7 @@ import torch
 from ..gguf import quants as Q
 from ..ops.attention import AttentionWorkspace, PagedKVCache, paged_attention
 from ..ops.linear import GemmWorkspace, QLinear
+from ..parallel.tp import split_cols, split_rows
 from ..ops.moe import MoeExperts, MoeWorkspace, moe_experts, moe_experts_ep, moe_route
 from ..utils.ext import C
 from .config import ModelConfig, rope_inv_freq
@@ -62,12 +63,23 @@ class _GpuLayer:
 
 class LlamaGPU:
     def __init__(self, cfg: ModelConfig, source, device, layer_range: tuple[int, int] | None = None,
-                 kv_layer_offset: int | None = None, ep=None):
+                 kv_layer_offset: int | None = None, ep=None, tp=None):
         """`ep`: an EpGroup (parallel/ep.py) -- this rank then holds only its
         share of every MoE layer's experts and exchanges tokens with the
-        other ranks inside each MoE layer."""
+        other ranks inside each MoE layer.  `tp`: a TpGroup (parallel/tp.py)
+        -- this rank holds n_heads/W query heads, n_kv/W KV heads and ffn/W
+        FFN features; o_proj/down_proj partials are summed over the group by
+        the GEMM epilogues."""
         self.cfg = cfg
         self.ep = ep
+        self.tp = tp
+        W = tp.world if tp else 1
+        tr = tp.rank if tp else 0
+        assert cfg.n_heads % W == 0 and cfg.n_kv_heads % W == 0 and cfg.ffn % W == 0
+        self.n_q, self.n_kv, self.ffn_loc = cfg.n_heads // W, cfg.n_kv_heads // W, cfg.ffn // W
+        if tp is not None:
+            assert not cfg.n_experts and not cfg.full_attn_interval, \
+                "tensor parallelism covers the dense attention + SwiGLU families"
         self.device = torch.device(device)
         lo, hi = layer_range or (0, cfg.n_layers)
         self.lo, self.hi = lo, hi
@@ -105,18 +117,29 @@ class LlamaGPU:
                 parts = [get(b + n) for n in ("attn_q.weight", "attn_k.weight", "attn_v.weight")]
                 qt = parts[0][1]
                 assert all(p[1] == qt for p in parts), "q/k/v must share a quant type"
-                rows = sum(p[2][0] for p in parts)
-                L.wqkv = QLinear(torch.cat([p[0] for p in parts]), qt, rows, H, dev)
+                d = cfg.head_dim
+                qh = 2 * d if cfg.attn_output_gate else d
+                shares = ((tr * self.n_q * qh, (tr + 1) * self.n_q * qh),
+                          (tr * self.n_kv * d, (tr + 1) * self.n_kv * d),
+                          (tr * self.n_kv * d, (tr + 1) * self.n_kv * d))
+                pieces = [split_rows(p[0], qt, p[2], a, z) if W > 1 else p[0]
+                          for p, (a, z) in zip(parts, shares)]
+                rows = sum(z - a for a, z in shares)
+                L.wqkv = QLinear(torch.cat(pieces), qt, rows, H, dev)
                 L.qkv_bias = None
                 if cfg.attn_bias:
-                    L.qkv_bias = torch.cat([small(b + n) for n in
-                                            ("attn_q.bias", "attn_k.bias", "attn_v.bias")])
+                    L.qkv_bias = torch.cat([small(b + n)[a:z] for n, (a, z) in
+                                            zip(("attn_q.bias", "attn_k.bias", "attn_v.bias"),
+                                                shares)])
                 t, qt, shape = get(b + "attn_output.weight")
-                L.wo = QLinear(t, qt, shape[0], shape[1], dev)
+                if W > 1:
+                    t = split_cols(t, qt, shape, tr * self.n_q * d, (tr + 1) * self.n_q * d)
+                L.wo = QLinear(t, qt, shape[0], self.n_q * d, dev)
                 L.o_bias = small(b + "attn_output.bias") if cfg.attn_bias else None
                 L.q_norm = small(b + "attn_q_norm.weight") if cfg.qk_norm else None
                 L.k_norm = small(b + "attn_k_norm.weight") if cfg.qk_norm else None
-                L.sinks = small(b + "attn_sinks.weight") if cfg.attn_sinks else None
+                L.sinks = (small(b + "attn_sinks.weight")[tr * self.n_q:(tr + 1) * self.n_q]
+                           .contiguous() if cfg.attn_sinks else None)
                 L.window = cfg.sliding_window if cfg.is_swa(i) else 0
                 L.gated = cfg.attn_output_gate
             L.experts = None
@@ -124,9 +147,20 @@ class LlamaGPU:
                 self._load_moe(L, b, get, small)
             else:
                 g, u = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
-                L.wgu = QLinear(torch.cat([g[0], u[0]]), g[1], 2 * cfg.ffn, H, dev)
+                F = self.ffn_loc
+                if W > 1:
+                    gp = split_rows(g[0], g[1], g[2], tr * F, (tr + 1) * F)
+                    up = split_rows(u[0], u[1], u[2], tr * F, (tr + 1) * F)
+                else:
+                    gp, up = g[0], u[0]
+                L.wgu = QLinear(torch.cat([gp, up]), g[1], 2 * F, H, dev)
                 t, qt, shape = get(b + "ffn_down.weight")
-                L.wdown = QLinear(t, qt, shape[0], shape[1], dev)
+                if W > 1:
+                    t = split_cols(t, qt, shape, tr * F, (tr + 1) * F)
+                L.wdown = QLinear(t, qt, shape[0], F, dev)
+                if W > 1:
+                    assert L.wo.kind == "q4k" and L.wdown.kind == "q4k", \
+                        "row-parallel layers run on the fused Q4_K tensor-core GEMM"
             self.layers.append(L)
         self.n_kv_layers, self.n_lin_layers = n_attn, n_lin
         self.next_norm = None
@@ -227,6 +261,11 @@ class LlamaGPU:
             r = max(r, (2 * c.ssm_k_heads + c.ssm_v_heads) * c.ssm_head_dim)
         return r
 
+    def _row_parallel(self, lin, x, ctx):
+        if self.tp is None:
+            return lin(x, ctx.gemm)
+        return self.tp.row_parallel(lin, x, ctx.gemm.status, ctx.gemm.num_sms)
+
     def _deltanet(self, L, b, kv, ctx, x, N):
         """Gated DeltaNet token mixing of one layer -> ctx.ssm_out (fp16)."""
         cfg = self.cfg
@@ -269,7 +308,9 @@ class LlamaGPU:
                 h_in: torch.Tensor | None = None) -> torch.Tensor:
         cfg = self.cfg
         N = b.tokens.shape[0]
-        H, nq, nkv, d = cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        H, nq, nkv, d = cfg.hidden, self.n_q, self.n_kv, cfg.head_dim
+        if self.tp is not None:
+            self.tp.begin_forward()
         h = ctx.h[:N]
         if self.first:
             C().embed_gather(self.embd, self.embd_type, H, b.tokens, h)
@@ -298,7 +339,7 @@ class LlamaGPU:
                                 num_sms=ctx.gemm.num_sms, groups=b.groups)
                 if gate is not None:
                     C().mul_f16(ao, gate)
-                g = L.wo(ao, ctx.gemm)
+                g = self._row_parallel(L.wo, ao, ctx)
                 C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
             if j + 1 < len(self.layers):
                 nxt_w, nxt_out = self.layers[j + 1].attn_norm, x
@@ -324,8 +365,8 @@ class LlamaGPU:
                     moe_experts(x, L.experts, ctx.moe, h, nxt_w, nxt_out, cfg.rms_eps, sh, shg)
                 continue
             g = L.wgu(x, ctx.gemm)
-            C().epi_swiglu(g, None, cfg.ffn, 0, False, 0.0, 0.0, act)
-            g = L.wdown(act, ctx.gemm)
+            C().epi_swiglu(g, None, self.ffn_loc, 0, False, 0.0, 0.0, act)
+            g = self._row_parallel(L.wdown, act, ctx)
             C().epi_residual_rmsnorm(g, h, None, nxt_w if nxt_w is not None else ctx.dummy_norm,
                                      nxt_out, cfg.rms_eps)
         if not self.last:
@@ -351,19 +392,23 @@ class GpuForwardContext:
         # them (router logits, shared-expert gate, DeltaNet beta/decay)
         side_rows = max(cfg.n_experts, 2 * cfg.ssm_v_heads, 1)
         self.gemm_side = GemmWorkspace(dev, max_tokens, side_rows, self.gemm.num_sms)
-        self.attn = AttentionWorkspace(dev, max_tokens, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim,
+        self.attn = AttentionWorkspace(dev, max_tokens, model.n_q, model.n_kv, cfg.head_dim,
                                        max_len, self.gemm.num_sms)
+        if model.tp is not None:
+            model.tp.setup(self.gemm.ws.numel())
         H = cfg.hidden
         self.h = torch.zeros(max_tokens, H, dtype=torch.float32, device=dev)
         self.x = torch.zeros(max_tokens, H, dtype=torch.float16, device=dev)
-        self.q = torch.zeros(max_tokens, cfg.n_heads, cfg.head_dim, dtype=torch.float16, device=dev)
-        self.attn_out = torch.zeros(max_tokens, cfg.q_dim, dtype=torch.float16, device=dev)
-        self.act = torch.zeros(max_tokens, cfg.ffn, dtype=torch.float16, device=dev)
+        self.q = torch.zeros(max_tokens, model.n_q, cfg.head_dim, dtype=torch.float16, device=dev)
+        self.attn_out = torch.zeros(max_tokens, model.n_q * cfg.head_dim, dtype=torch.float16,
+                                    device=dev)
+        self.act = torch.zeros(max_tokens, model.ffn_loc, dtype=torch.float16, device=dev)
         self.xs = torch.zeros(max_samples, H, dtype=torch.float16, device=dev)
         self.logits = torch.zeros(max_samples, cfg.vocab, dtype=torch.float32, device=dev)
         self.dummy_norm = torch.ones(H, dtype=torch.float32, device=dev)
         if cfg.attn_output_gate:
-            self.gate = torch.zeros(max_tokens, cfg.q_dim, dtype=torch.float16, device=dev)
+            self.gate = torch.zeros(max_tokens, model.n_q * cfg.head_dim, dtype=torch.float16,
+                                    device=dev)
         if model.n_lin_layers:
             nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
             self.ssm_qkv = torch.zeros(max_tokens, (2 * nk + nv) * dh, dtype=torch.float32,

@@ -1,0 +1,76 @@
+"""Tensor parallelism with the fused GEMM + peer-memory reduction (2 GPUs):
+the TP2 model's logits equal the single-GPU model's.  Skipped with fewer
+than two GPUs."""
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _batch(tokens, positions, bt, device, sample_rows):
+    from swarmllm_b200.models.llama import StepBatch
+    t = lambda a, dt=torch.int32: torch.as_tensor(np.asarray(a), dtype=dt, device=device)
+    return StepBatch(t(tokens), t(positions), t(positions), t(bt), t(np.asarray(positions) + 1),
+                     t(sample_rows, torch.int64), 256)
+
+
+def _worker(rank, world, port):
+    import torch.distributed as dist
+    from swarmllm_b200.models.config import ModelConfig
+    from swarmllm_b200.models.llama import LlamaGPU
+    from swarmllm_b200.models.weights import RandomSource
+    from swarmllm_b200.ops.attention import PagedKVCache
+    from swarmllm_b200.parallel.tp import TpGroup
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        cfg = ModelConfig(name="t", arch="llama", n_layers=3, hidden=512, n_heads=8, n_kv_heads=2,
+                          head_dim=64, ffn=1024, vocab=1024, weight_qtype="Q4_K",
+                          embed_qtype="F16", output_qtype="Q4_K")
+        tp = TpGroup(rank, world, dev)
+        m_tp = LlamaGPU(cfg, RandomSource(cfg, seed=3), dev, tp=tp)
+        m_1 = LlamaGPU(cfg, RandomSource(cfg, seed=3), dev)
+        c_tp, c_1 = m_tp.make_context(64, 64, 256), m_1.make_context(64, 64, 256)
+        kv_tp = PagedKVCache(cfg.n_layers, 8, m_tp.n_kv, cfg.head_dim, dev)
+        kv_1 = PagedKVCache(cfg.n_layers, 8, cfg.n_kv_heads, cfg.head_dim, dev)
+        rng = np.random.default_rng(0)
+        toks = rng.integers(0, cfg.vocab, 43)
+        bt = np.tile(np.arange(8, dtype=np.int32), (64, 1))
+        for lo, hi in ((0, 40), (40, 41), (41, 42), (42, 43)):
+            pos = np.arange(lo, hi)
+            rows = list(range(hi - lo))
+            a = m_tp.forward(_batch(toks[lo:hi], pos, bt[:hi - lo], dev, rows), kv_tp, c_tp)
+            b = m_1.forward(_batch(toks[lo:hi], pos, bt[:hi - lo], dev, rows), kv_1, c_1)
+            torch.cuda.synchronize(dev)
+            c_tp.gemm.check()
+            cos = torch.nn.functional.cosine_similarity(a.double(), b.double(), dim=-1)
+            assert float(cos.min()) > 0.9999, (rank, lo, cos)
+            rel = float((a - b).norm() / b.norm())
+            assert rel < 1e-3, (rank, lo, rel)
+        tp.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_matches_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)
