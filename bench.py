@@ -46,6 +46,8 @@ def parse():
     p.add_argument("--gen", type=int, default=512)
     p.add_argument("--ttft-reps", type=int, default=3)
     p.add_argument("--chunk", type=int, default=0, help="prefill chunk (0: whole prompt)")
+    p.add_argument("--tp", type=int, default=0,
+                   help="tensor-parallel ranks per pipeline stage (0: 2 on 8 GPUs, else 1)")
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the headline)")
     return p.parse_args()
 
@@ -229,6 +231,8 @@ def main():
         from swarmllm_b200.parallel.bench_ep import ep_bench
         return ep_bench(args)
     from swarmllm_b200.parallel.bench_pp import pipeline_bench
+    if not args.tp:  # PP 2/4 stages, PP4 x TP2 on the 8-GPU runs
+        args.tp = 2 if args.gpus >= 8 else 1
     return pipeline_bench(args)
 
 

@@ -291,6 +291,8 @@ class LlamaGPU:
                 n += 7   # in GEMM, conv, ba GEMM, z GEMM, delta rule, out GEMM, residual+norm
             else:
                 n += 6 + (1 if L.gated else 0)  # qkv GEMM, rope/KV, attention + combine, o GEMM, residual+norm
+            if self.tp is not None:
+                n += 2   # flag waits after the two row-parallel GEMMs
             if L.experts is not None:
                 # router GEMM + top-k, then plan/scatter/2 grouped GEMMs/combine, or under
                 # expert parallelism send-counts/dispatch/wait/plan/2 GEMMs/wait/combine
@@ -394,8 +396,9 @@ class GpuForwardContext:
         self.gemm_side = GemmWorkspace(dev, max_tokens, side_rows, self.gemm.num_sms)
         self.attn = AttentionWorkspace(dev, max_tokens, model.n_q, model.n_kv, cfg.head_dim,
                                        max_len, self.gemm.num_sms)
-        if model.tp is not None:
-            model.tp.setup(self.gemm.ws.numel())
+        if model.tp is not None:  # receive buffers for the row-parallel (hidden-wide) GEMMs
+            from ..ops.linear import stream_k_floats
+            model.tp.setup(stream_k_floats(max_tokens, cfg.hidden, self.gemm.num_sms))
         H = cfg.hidden
         self.h = torch.zeros(max_tokens, H, dtype=torch.float32, device=dev)
         self.x = torch.zeros(max_tokens, H, dtype=torch.float16, device=dev)

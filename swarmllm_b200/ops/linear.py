@@ -21,6 +21,19 @@ from ..gguf import quants as Q
 from ..utils.ext import C
 
 
+def stream_k_floats(max_tokens: int, rows: int, num_sms: int) -> int:
+    """fp32 floats of stream-K partial slots any GEMM of <= max_tokens rows x
+    `rows` outputs needs: (tiles + CTAs) x tok_tile x 128, over every token tile."""
+    need = 0
+    for T in sorted({1, 16, 32, 64, 128, 256, max_tokens}):
+        if T > max_tokens:
+            continue
+        n_tok = C().q4k_tc_plan(128, 256, T, num_sms)[0]
+        tiles = (rows + 127) // 128 * ((T + n_tok - 1) // n_tok)
+        need = max(need, (tiles + num_sms) * n_tok * 128)
+    return need
+
+
 class GemmWorkspace:
     """Scratch shared by every GEMM of one forward: the stream-K partial
     buffer, a dense fallback buffer and the kernel status word."""
@@ -34,14 +47,8 @@ class GemmWorkspace:
         props = torch.cuda.get_device_properties(self.device)
         self.num_sms = num_sms or props.multi_processor_count
         # Stream-K slots: (tiles + CTAs) x tok_tile x 128 floats, CTAs <= num_sms.
-        need = 0
-        for mt, rows in ((max_tokens, max_rows),) + tuple(extra):
-            for T in sorted({1, 16, 32, 64, 128, 256, mt}):
-                if T > mt:
-                    continue
-                n_tok = C().q4k_tc_plan(128, 256, T, self.num_sms)[0]
-                tiles = (rows + 127) // 128 * ((T + n_tok - 1) // n_tok)
-                need = max(need, (tiles + self.num_sms) * n_tok * 128)
+        need = max(stream_k_floats(mt, rows, self.num_sms)
+                   for mt, rows in ((max_tokens, max_rows),) + tuple(extra))
         self.ws = torch.empty(int(need), dtype=torch.float32, device=self.device)
         self._dense = torch.empty(0, dtype=torch.float32, device=self.device)
         self.status = torch.zeros(8, dtype=torch.int32, device=self.device)

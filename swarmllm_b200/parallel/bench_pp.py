@@ -36,13 +36,15 @@ def pipeline_bench(args):
     cfg = preset(args.model)
     if args.layers:
         cfg = cfg.scaled(n_layers=args.layers)
-    B = args.batch * world
+    tp = getattr(args, "tp", 1) or 1
+    n_stages = world // tp
+    B = args.batch * n_stages
     P, G = args.prompt, args.gen
     ecfg = EngineConfig(max_model_len=P + G + 64, max_running=B, max_step_tokens=P,
                         prefill_chunk=P, kv_pages=B * ((P + G + 64 + 15) // 16) + 64)
     t0 = time.time()
     eng = PipelineEngine(cfg, ecfg, lambda: RandomSource(cfg, seed=1234, on_device=True), dev,
-                         micro_batches=world)
+                         micro_batches=n_stages, tp=tp)
     torch.cuda.synchronize()
     dist.barrier()
     _log(rank, f"stages {eng.bounds}, init {time.time() - t0:.1f}s")
@@ -105,9 +107,8 @@ def pipeline_bench(args):
     ms_b, wall_b, clocks = decode(B)
     ms_1, wall_1, _ = decode(1)
     value = B * args.steps / (ms_b / 1e3)
-    layers_local = eng.hi - eng.lo
-    launches = torch.tensor([(2 + 10 * layers_local + (3 if eng.last else 0)) * world * args.steps],
-                            device=dev)
+    # every rank runs its stage's forward once per micro-batch
+    launches = torch.tensor([eng.model.decode_launches() * eng.micro * args.steps], device=dev)
     dist.all_reduce(launches)
     if rank == 0:
         line = {
@@ -119,8 +120,11 @@ def pipeline_bench(args):
             "dtype": "fp16 activations, fp32 accumulate, Q4_K weights",
             "data": "synthetic uniform-random token ids; random-init Q4_K weights (llama-3.3-70b architecture)",
             "config": {"model": cfg.name, "layers": cfg.n_layers, "global_batch": B, "seq_len": P,
-                       "gen_len": G, "parallelism": f"pp{world}", "stages": eng.bounds,
-                       "micro_batches": world, "kv": "paged fp16, 16-token pages",
+                       "gen_len": G,
+                       "parallelism": f"pp{n_stages}" + (f"xtp{tp}" if tp > 1 else ""),
+                       "stages": eng.bounds, "micro_batches": eng.micro,
+                       "tp": "fused: GEMM epilogue pushes partials over NVLink" if tp > 1 else None,
+                       "kv": "paged fp16, 16-token pages",
                        "l2": "no flush: weights streamed per step >> 126 MB L2"},
             "decode_tok_s_batch1": round(args.steps / (ms_1 / 1e3), 2),
             "ttft_p50_ms": round(statistics.median(ttfts[1:]), 2), "ttft_prompt_tokens": P,

@@ -66,26 +66,41 @@ class PipelineEngine:
     in lockstep; only rank 0 accepts requests and returns results."""
 
     def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, source_factory, device,
-                 group=None, micro_batches: int | None = None, use_graphs: bool = True):
+                 group=None, micro_batches: int | None = None, use_graphs: bool = True,
+                 tp: int = 1):
+        """`tp` > 1: every stage is a tensor-parallel group of `tp` consecutive
+        ranks (stage = rank // tp, lane = rank % tp); activations go from a
+        lane of one stage to the same lane of the next."""
         self.cfg, self.ecfg = cfg, ecfg
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        assert self.world % tp == 0
+        self.tp, self.lane = tp, self.rank % tp
+        self.stage, self.n_stages = self.rank // tp, self.world // tp
         self.device = torch.device(device)
         self.gpu = self.device.type == "cuda"
-        self.bounds = stage_bounds(cfg.n_layers, self.world, 0.5, 1.0)
-        lo, hi = self.bounds[self.rank], self.bounds[self.rank + 1]
+        self.bounds = stage_bounds(cfg.n_layers, self.n_stages, 0.5, 1.0)
+        lo, hi = self.bounds[self.stage], self.bounds[self.stage + 1]
         self.lo, self.hi = lo, hi
-        self.first, self.last = self.rank == 0, self.rank == self.world - 1
-        self.micro = micro_batches or self.world
+        self.root = self.rank == 0  # owns the scheduler and the KV block manager
+        self.first, self.last = self.stage == 0, self.stage == self.n_stages - 1
+        self.micro = micro_batches or self.n_stages
+        self.tpg = None
+        if tp > 1:
+            from .tp import TpGroup
+            groups = [dist.new_group(list(range(s * tp, (s + 1) * tp)))
+                      for s in range(self.n_stages)]
+            self.tpg = TpGroup(self.lane, tp, device, groups[self.stage])
         src = source_factory()
         ps = ecfg.page_size
         self.max_pages = (ecfg.max_model_len + ps - 1) // ps
         pages = ecfg.kv_pages or ecfg.max_running * self.max_pages
         if self.gpu:
             from ..models.llama import LlamaGPU
-            self.model = LlamaGPU(cfg, src, self.device, (lo, hi))
-            self.kv = PagedKVCache(hi - lo, pages + 1, cfg.n_kv_heads, cfg.head_dim, self.device, ps)
+            self.model = LlamaGPU(cfg, src, self.device, (lo, hi), tp=self.tpg)
+            self.kv = PagedKVCache(hi - lo, pages + 1, self.model.n_kv, cfg.head_dim, self.device,
+                                   ps)
             mt = ecfg.max_step_tokens
             self.ctx = self.model.make_context(mt, max(ecfg.max_running, 1), ecfg.max_model_len)
             self.sampler = DeviceSampler(self.device, max(ecfg.max_running, 1))
@@ -96,7 +111,7 @@ class PipelineEngine:
                                    dtype=torch.float32)
             self.ctx = None
         self.trash_page = pages
-        if self.first:
+        if self.root:
             N = native()
             self.bm = N.BlockManager(pages, ps, ecfg.prefix_cache)
             self.sched = N.Scheduler(self.bm, ecfg.max_step_tokens, ecfg.max_running,
@@ -111,7 +126,7 @@ class PipelineEngine:
 
     # ------------------------------------------------------------------ requests (rank 0)
     def add_request(self, prompt_ids, params: SamplingParams | None = None) -> int:
-        assert self.first, "requests enter at rank 0"
+        assert self.root, "requests enter at rank 0"
         params = params or SamplingParams()
         rid = next(self._ids)
         eos = -1 if params.ignore_eos else params.eos_token_id
@@ -126,7 +141,7 @@ class PipelineEngine:
     def _bcast_plan(self, plan):
         """Rank 0 packs the step into one int32 tensor; everyone unpacks."""
         dev = self.device if self.gpu else torch.device("cpu")
-        if self.first:
+        if self.root:
             tokens, positions, slots, bt_rows, seq_lens, sample_rows = plan_arrays(
                 plan, self.bm, self.max_pages)
             N = len(tokens)
@@ -143,10 +158,10 @@ class PipelineEngine:
         dist.broadcast(hdr, 0, group=self.group)
         N, B, mp = [int(v) for v in hdr.cpu()]
         size = 4 * N + 3 * B + N * mp
-        buf = torch.from_numpy(body).to(dev) if self.first else torch.zeros(size, dtype=torch.int32, device=dev)
+        buf = torch.from_numpy(body).to(dev) if self.root else torch.zeros(size, dtype=torch.int32, device=dev)
         if size:
             dist.broadcast(buf, 0, group=self.group)
-        b = buf.cpu().numpy() if not self.first else body
+        b = buf.cpu().numpy() if not self.root else body
         o = 0
 
         def take(n):
@@ -171,7 +186,7 @@ class PipelineEngine:
 
     # ------------------------------------------------------------------ step
     def step(self):
-        plan = self.sched.schedule() if self.first else None
+        plan = self.sched.schedule() if self.root else None
         tokens, positions, slots, seq_lens, seq_start, seq_ntok, seq_samp, bt = self._bcast_plan(plan)
         N, B = len(tokens), len(seq_start)
         if N == 0:
@@ -192,14 +207,14 @@ class PipelineEngine:
             h_in = None
             if not self.first:
                 h_in = torch.empty(rows, H, dtype=self.comm_dtype, device=dev)
-                dist.recv(h_in, self.rank - 1, group=self.group)
+                dist.recv(h_in, self.rank - self.tp, group=self.group)
             out = self.model.forward(batch, self.kv, self.ctx, h_in)
             if not self.last:
                 # own buffer: the model's activation buffer is reused by the next micro-batch
                 h = out.to(self.comm_dtype).clone()
-                req = dist.isend(h, self.rank + 1, group=self.group)
+                req = dist.isend(h, self.rank + self.tp, group=self.group)
                 pending.append((req, h))
-            elif mb.n_sample:
+            elif mb.n_sample and self.lane == 0:
                 if self.record_logits is not None:
                     self.record_logits.append(out.detach().float().cpu().clone())
                 params = self._params_for(mb.seqs, seq_samp)
@@ -212,16 +227,17 @@ class PipelineEngine:
         # 2 ranks the pair (0, 1) carries both directions in one ordered NCCL
         # stream, and per-micro-batch token sends would wait on activation sends.
         n_samp_total = sum(mb.n_sample for mb in mbs)
-        if self.last and self.world > 1 and n_samp_total:
+        last_lane0 = (self.n_stages - 1) * self.tp  # global rank that samples
+        if self.last and self.lane == 0 and not self.root and n_samp_total:
             dist.send(torch.cat(sampled_all).contiguous(), 0, group=self.group)
         for req, _ in pending:
             req.wait()
-        if self.first:
-            if self.world > 1:
+        if self.root:
+            if last_lane0 != 0:
                 sampled = np.zeros(0, np.int32)
                 if n_samp_total:
                     tok = torch.empty(n_samp_total, dtype=torch.int32, device=dev)
-                    dist.recv(tok, self.world - 1, group=self.group)
+                    dist.recv(tok, last_lane0, group=self.group)
                     sampled = tok.cpu().numpy()
             else:
                 sampled = (torch.cat(sampled_all).cpu().numpy() if sampled_all
@@ -245,7 +261,7 @@ class PipelineEngine:
         return [ps[s] for s in seqs if seq_samp[s]]
 
     def has_work(self) -> bool:
-        flag = torch.tensor([1 if (self.first and self.sched.has_work()) else 0], dtype=torch.int32,
+        flag = torch.tensor([1 if (self.root and self.sched.has_work()) else 0], dtype=torch.int32,
                             device=self.device if self.gpu else "cpu")
         dist.broadcast(flag, 0, group=self.group)
         return bool(flag.item())
@@ -255,13 +271,13 @@ class PipelineEngine:
         the generated tokens (other ranks return None)."""
         params = params or SamplingParams()
         res = {}
-        if self.first:
+        if self.root:
             rids = [self.add_request(p, params) for p in prompts]
             res = {r: [] for r in rids}
         while self.has_work():
             for rid, tok, fin in self.step():
                 res[rid].append(tok)
-        if self.first:
+        if self.root:
             return [res[r] for r in sorted(res)]
         return None
 
