@@ -1,0 +1,88 @@
+"""Standalone cases of the hot kernels, for profiling one kernel at a time:
+
+    python -m swarmllm_b200.utils.kernel_cases {qgemm|dense|attn|moe|delta}
+
+Each case builds benchmark-sized operands on cuda:0 (inputs larger than the
+126 MB L2 where memory traffic matters), runs the kernel a few times and
+exits.  Under ncu, capture one launch after the warm-up ones, e.g.
+
+    ncu --set full --clock-control none -k regex:qgemm_q4k -s 2 -c 1 \
+        -o prof_qgemm python -m swarmllm_b200.utils.kernel_cases qgemm
+"""
+import sys, math
+import numpy as np, torch
+from swarmllm_b200.utils.ext import C
+from swarmllm_b200.gguf import quants as Q
+dev = "cuda:0"
+which = sys.argv[1] if len(sys.argv) > 1 else "qgemm"
+torch.manual_seed(0)
+
+def rand_q4k(rows, K):
+    # random Q4_K blocks generated on the device (valid scales)
+    from swarmllm_b200.models.weights import _random_blocks_device
+    return _random_blocks_device("w", (rows, K), Q.Q4_K, 1, 0.02, dev)
+
+if which == "qgemm":       # Llama-3.3-70B gate|up at decode batch 32 (264 MB of weights)
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    rows, K, T = 57344, 8192, 32
+    lin = QLinear(rand_q4k(rows, K), Q.Q4_K, rows, K, dev)
+    ws = GemmWorkspace(dev, T, rows)
+    x = torch.randn(T, K, device=dev).half()
+    for _ in range(5): lin(x, ws)
+elif which == "dense":     # gpt-oss LM head (201088 x 2880 fp16, 1.16 GB) at batch 16
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    rows, K, T = 201088, 2880, 16
+    w = (torch.randn(rows, K, device=dev) * 0.02).half()
+    lin = QLinear(w.view(torch.uint8).reshape(-1), Q.F16, rows, K, dev)
+    ws = GemmWorkspace(dev, T, rows)
+    x = torch.randn(T, K, device=dev).half()
+    for _ in range(5): lin(x, ws)
+elif which == "attn":      # decode batch 32, context 2300, 64 q / 8 kv heads, d 128 (300 MB KV)
+    from swarmllm_b200.ops.attention import AttentionWorkspace, paged_attention
+    B, L, nq, nkv, d, ps = 32, 2300, 64, 8, 128, 16
+    ppseq = (L + ps - 1) // ps
+    P = B * ppseq
+    K = torch.randn(P, nkv, ps, d, device=dev).half(); V = torch.randn_like(K)
+    bt = torch.arange(P, device=dev, dtype=torch.int32).view(B, ppseq)
+    lens = torch.full((B,), L, dtype=torch.int32, device=dev)
+    q = torch.randn(B, nq, d, device=dev).half()
+    ws = AttentionWorkspace(dev, B, nq, nkv, d, L + 64)
+    out = torch.empty_like(q)
+    for _ in range(5):
+        paged_attention(q, K, V, bt, lens, ws, out, L + 64, 1 / math.sqrt(d))
+elif which == "moe":       # gpt-oss-style experts (32 of 128, MXFP4), batch 64 tokens top-4
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    from swarmllm_b200.ops.moe import MoeExperts, MoeWorkspace, moe_ffn
+    from swarmllm_b200.models.weights import _random_blocks_device
+    E, k, H, F, T = 32, 4, 2880, 2880, 64
+    g = _random_blocks_device("g", (E, F, H), Q.MXFP4, 1, 0.02, dev).view(E, F, -1)
+    u = _random_blocks_device("u", (E, F, H), Q.MXFP4, 1, 0.02, dev).view(E, F, -1)
+    dn = _random_blocks_device("d", (E, H, F), Q.MXFP4, 1, 0.02, dev).view(E, H, -1)
+    ex = MoeExperts(g, u, dn, Q.MXFP4, H, F, dev, act_kind=1)
+    wr = (torch.randn(E, H, device=dev) * 0.1).half()
+    router = QLinear(wr.view(torch.uint8).reshape(-1), Q.F16, E, H, dev)
+    ws = MoeWorkspace(dev, T, H, F, E, k, ex.x_dtype, 148)
+    gws = GemmWorkspace(dev, T, E)
+    x = torch.randn(T, H, device=dev).half()
+    r = torch.zeros(T, H, device=dev)
+    for _ in range(5): moe_ffn(x, ex, router, None, ws, gws, r, None, None, 1e-5)
+elif which == "delta":     # Qwen3-Next-style DeltaNet prefill: 4096 tokens, 16 k / 32 v heads
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    T, nk, nv, D = 4096, 16, 32, 128
+    C_ = (2 * nk + nv) * D
+    qkv = torch.randn(T, C_, device=dev)
+    gws = GemmWorkspace(dev, T, 2 * nv)
+    x = torch.randn(T, 2048, device=dev).half()
+    wba = QLinear((torch.randn(2 * nv, 2048, device=dev) * 0.02).half().view(torch.uint8).reshape(-1), Q.F16, 2 * nv, 2048, dev)
+    wz = QLinear((torch.randn(nv * D, 2048, device=dev) * 0.02).half().view(torch.uint8).reshape(-1), Q.F16, nv * D, 2048, dev)
+    gws2 = GemmWorkspace(dev, T, nv * D)
+    gba, gz = wba(x, gws), wz(x, gws2)
+    A = -torch.rand(nv, device=dev); dtb = torch.rand(nv, device=dev)
+    nw = torch.ones(D, device=dev)
+    state = torch.zeros(2, nv, D, D, device=dev)
+    seqs = torch.tensor([[0, T, 1, 0]], dtype=torch.int32, device=dev)
+    oraw = torch.zeros(T, nv * D, device=dev); out = torch.zeros(T, nv * D, device=dev).half()
+    for _ in range(3):
+        C().delta_chunk(qkv, nk, nv, D, gba, dtb, A, gz, nw, 1e-6, state, seqs, 1, oraw, out)
+torch.cuda.synchronize()
+print("ok", which)
