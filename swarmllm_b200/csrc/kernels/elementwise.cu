@@ -20,6 +20,9 @@
 #include "gemm_out.cuh"
 #include "quant_blocks.cuh"
 
+#include <cooperative_groups.h>
+namespace cg = cooperative_groups;
+
 namespace swarm {
 
 __global__ void embed_gather_kernel(const uint8_t* __restrict__ table, int type, int hidden,
@@ -235,10 +238,67 @@ void launch_rmsnorm(const float* x, const float* w, __half* out, int rows, int d
   SW_LAUNCH_CHECK();
 }
 
+// Small batches: one thread-block cluster of kClusterNorm CTAs per token, each
+// CTA owning a contiguous slice of the row; the row's sum of squares is
+// reduced through distributed shared memory (every CTA reads the others'
+// partials), so a decode step's few tokens still spread over many SMs.
+constexpr int kClusterNorm = 8;
+
+__global__ void __launch_bounds__(256) epi_residual_rmsnorm_cluster_kernel(
+    GemmOut g, float* __restrict__ residual, const float* __restrict__ bias,
+    const float* __restrict__ w, __half* __restrict__ out, float eps, int out_stride) {
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float part;
+  __shared__ float red[32];
+  extern __shared__ float slice[];
+  const int cr = (int)cluster.block_rank(), cn = (int)cluster.num_blocks();
+  const int t = blockIdx.x / cn;
+  const int dim = g.rows;
+  const int per = (dim + cn - 1) / cn;
+  const int lo = cr * per, hi = min(dim, lo + per);
+  float* rr = residual + (size_t)t * dim;
+  float ss = 0.f;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float v = rr[i] + g.get(t, i) + (bias ? bias[i] : 0.f);
+    rr[i] = v;
+    slice[i - lo] = v;
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) part = ss;
+  cluster.sync();
+  float tot = 0.f;
+  for (int r = 0; r < cn; ++r) tot += *cluster.map_shared_rank(&part, r);
+  cluster.sync();  // peers finished reading `part` before any CTA exits
+  if (out == nullptr) return;
+  const float inv = rsqrtf(tot / dim + eps);
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x)
+    out[(size_t)t * out_stride + i] = __float2half_rn(slice[i - lo] * inv * w[i]);
+}
+
 void launch_epi_residual_rmsnorm(const GemmOut& g, float* residual, const float* bias,
                                  const float* w, __half* out, float eps, int out_stride,
                                  cudaStream_t s) {
   if (g.T <= 0) return;
+  if (g.T < 64) {
+    const int per = (g.rows + kClusterNorm - 1) / kClusterNorm;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(g.T * kClusterNorm);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t)per * sizeof(float);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kClusterNorm;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, epi_residual_rmsnorm_cluster_kernel, g, residual, bias, w, out, eps,
+                       out_stride ? out_stride : g.rows);
+    SW_LAUNCH_CHECK();
+    return;
+  }
   size_t sm = (size_t)g.rows * sizeof(float);
   if (sm > 48 * 1024)
     cudaFuncSetAttribute(epi_residual_rmsnorm_kernel<512>,

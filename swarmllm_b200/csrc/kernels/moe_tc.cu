@@ -33,6 +33,8 @@
 #include "ep_common.cuh"
 
 #include <type_traits>
+#include <cooperative_groups.h>
+namespace cg = cooperative_groups;
 
 namespace swarm {
 using namespace tc;
@@ -707,16 +709,73 @@ int launch_moe_gemm_tc(int fmt, int epi, const void* w, int rows, int K, const v
                               : moe_launch_fmt<kMoeFmtMX, kMoeEpiStore>(tok_tile, map, a, ctas, s);
 }
 
+// Small batches: a cluster of 8 CTAs per token splits the row; the RMSNorm's
+// sum of squares is reduced through distributed shared memory.
+__global__ void __launch_bounds__(256) moe_combine_cluster_kernel(
+    const float* __restrict__ rows, int row_stride, const float* __restrict__ wts, int k,
+    GemmOut sh, int has_sh, GemmOut shg, int has_shg, float* __restrict__ residual, int H,
+    const float* __restrict__ norm_w, __half* __restrict__ out, int out_stride, float eps) {
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float part;
+  __shared__ float red[32];
+  extern __shared__ float cslice[];
+  const int cr = (int)cluster.block_rank(), cn = (int)cluster.num_blocks();
+  const int t = blockIdx.x / cn;
+  const int per = (H + cn - 1) / cn;
+  const int lo = cr * per, hi = min(H, lo + per);
+  float gate = 1.f;
+  if (has_shg) gate = 1.f / (1.f + __expf(-shg.get(t, 0)));
+  float ss = 0.f;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    float v = 0.f;
+    for (int j = 0; j < k; ++j) v += wts[t * k + j] * rows[(size_t)(t * k + j) * row_stride + i];
+    if (has_sh) v += gate * sh.get(t, i);
+    const float r = residual[(size_t)t * H + i] + v;
+    residual[(size_t)t * H + i] = r;
+    cslice[i - lo] = r;
+    ss += r * r;
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) part = ss;
+  cluster.sync();
+  float tot = 0.f;
+  for (int r = 0; r < cn; ++r) tot += *cluster.map_shared_rank(&part, r);
+  cluster.sync();
+  if (out == nullptr) return;
+  const float inv = rsqrtf(tot / H + eps);
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x)
+    out[(size_t)t * out_stride + i] = __float2half_rn(cslice[i - lo] * inv * norm_w[i]);
+}
+
 int launch_moe_combine(const float* rows, int row_stride, const float* wts, int k,
                        const GemmOut* sh, const GemmOut* shg, float* residual, int T, int H,
                        const float* norm_w, __half* out, int out_stride, float eps,
                        cudaStream_t s) {
   if (T <= 0) return 0;
+  GemmOut z{};
+  if (T < 64) {
+    constexpr int kC = 8;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(T * kC);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t)((H + kC - 1) / kC) * sizeof(float);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kC;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, moe_combine_cluster_kernel, rows, row_stride, wts, k,
+                       sh ? *sh : z, (int)(sh != nullptr), shg ? *shg : z, (int)(shg != nullptr),
+                       residual, H, norm_w, out, out_stride ? out_stride : H, eps);
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+  }
   const size_t smem = (size_t)H * 4;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(moe_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem);
-  GemmOut z{};
   moe_combine_kernel<<<T, 512, smem, s>>>(rows, row_stride, wts, k, sh ? *sh : z, sh != nullptr,
                                           shg ? *shg : z, shg != nullptr, residual, H, norm_w,
                                           out, out_stride ? out_stride : H, eps);
