@@ -1,0 +1,158 @@
+"""Failure detection and recovery for the pipeline-parallel engine.
+
+A control TCPStore (hosted by the root rank, separate from the process
+groups) outlives every process group.  Ranks heartbeat into it once per
+engine step.  When a collective fails -- a peer's process died (gloo reports
+the closed connection at once) or stopped answering (the group's short
+timeout) -- or the root sees a stale heartbeat:
+
+  1. every survivor drops the broken process group and registers itself
+     under the next membership epoch;
+  2. the root waits a grace period, fixes the membership (the ranks that
+     registered) and publishes it;
+  3. the survivors form a new process group through a store prefix for that
+     epoch and rebuild the pipeline over the survivors: new stage boundaries
+     from the layer planner, each rank reloading its new layer range;
+  4. the root replays every unfinished request as (prompt + tokens generated
+     so far) with the remaining token budget: the lost KV is recomputed, so
+     greedy output is identical to an undisturbed run.
+
+The root holds the scheduler; if the root itself fails the requests are lost
+(the client retries), as when the reference's coordinator fails.
+
+Reference behaviour: HealthMonitor pings and missed-ping death
+(src/health/monitor.rs:702-704,904), router retry with re-planning
+(src/inference/router/mod.rs:524,598,659), failover_segment onto standbys and
+replay of retained activations (src/inference/pipeline/distributed.rs:2461).
+"""
+from __future__ import annotations
+
+import datetime
+import time
+from dataclasses import dataclass, field
+
+import torch.distributed as dist
+
+from ..engine.sampling import SamplingParams
+
+
+@dataclass
+class _Req:
+    prompt: list
+    params: SamplingParams
+    out: list = field(default_factory=list)
+    done: bool = False
+
+
+class RankFailure(RuntimeError):
+    pass
+
+
+class ResilientPipeline:
+    def __init__(self, build_engine, rank: int, world: int, ctl_host: str, ctl_port: int,
+                 backend: str = "gloo", pg_timeout_s: float = 10.0, grace_s: float | None = None,
+                 heartbeat_stale_s: float = 30.0):
+        """`build_engine()` returns a PipelineEngine over the current default
+        process group; it is called again after every re-plan."""
+        self.rank, self.world0 = rank, world
+        self.backend, self.pg_timeout_s = backend, pg_timeout_s
+        # a survivor that only learns of the failure from the group timeout
+        # must still register before the root fixes the membership
+        self.grace_s = grace_s if grace_s is not None else pg_timeout_s + 2.0
+        self.stale_s = heartbeat_stale_s
+        self.store = dist.TCPStore(ctl_host, ctl_port, world, rank == 0,
+                                   timeout=datetime.timedelta(seconds=60))
+        self.members = list(range(world))
+        self.epoch = 0
+        self.build_engine = build_engine
+        self.recoveries = 0
+        self._form_group()
+        self.eng = build_engine()
+
+    # ------------------------------------------------------------------ membership
+    @property
+    def root(self) -> bool:
+        return self.rank == self.members[0]
+
+    def _form_group(self):
+        pre = dist.PrefixStore(f"pg{self.epoch}", self.store)
+        dist.init_process_group(self.backend, store=pre, rank=self.members.index(self.rank),
+                                world_size=len(self.members),
+                                timeout=datetime.timedelta(seconds=self.pg_timeout_s))
+
+    def _heartbeat(self, step: int):
+        self.store.set(f"hb/{self.rank}", f"{step}:{time.time()}")
+
+    def stale_ranks(self) -> list[int]:
+        """Members whose last heartbeat is older than the staleness limit."""
+        now, bad = time.time(), []
+        for r in self.members:
+            if r == self.rank:
+                continue
+            try:
+                ts = float(self.store.get(f"hb/{r}").decode().split(":")[1])
+            except Exception:
+                continue
+            if now - ts > self.stale_s:
+                bad.append(r)
+        return bad
+
+    def _recover(self):
+        self.recoveries += 1
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+        self.epoch += 1
+        self.store.set(f"alive/{self.epoch}/{self.rank}", "1")
+        key = f"members/{self.epoch}"
+        if self.rank == self.members[0]:
+            time.sleep(self.grace_s)
+            alive = [r for r in self.members
+                     if self.store.check([f"alive/{self.epoch}/{r}"])]
+            self.store.set(key, ",".join(map(str, alive)))
+        self.store.wait([key], datetime.timedelta(seconds=60))
+        self.members = [int(x) for x in self.store.get(key).decode().split(",")]
+        if self.rank not in self.members:
+            raise RankFailure("this rank was dropped from the membership")
+        self._form_group()
+        self.eng = self.build_engine()
+
+    # ------------------------------------------------------------------ generation
+    def generate(self, prompts: list[list[int]], params: SamplingParams | None = None,
+                 max_recoveries: int = 3):
+        """Collective over the survivors; the root returns the token lists."""
+        params = params or SamplingParams()
+        reqs = [_Req(list(p), params) for p in prompts] if self.root else []
+        step = 0
+        while True:
+            try:
+                rid_of = {}
+                if self.root:
+                    for i, r in enumerate(reqs):
+                        left = r.params.max_tokens - len(r.out)
+                        if r.done or left <= 0:
+                            r.done = True
+                            continue
+                        sp = SamplingParams(**{**r.params.__dict__, "max_tokens": left})
+                        rid_of[self.eng.add_request(r.prompt + r.out, sp)] = i
+                while self.eng.has_work():
+                    for rid, tok, fin in self.eng.step():
+                        r = reqs[rid_of[rid]]
+                        r.out.append(tok)
+                        r.done = r.done or fin
+                    step += 1
+                    self._heartbeat(step)
+                    if self.root and self.stale_ranks():
+                        raise RankFailure(f"stale heartbeat: {self.stale_ranks()}")
+                return [r.out for r in reqs] if self.root else None
+            except (RuntimeError, dist.DistBackendError):
+                if self.recoveries >= max_recoveries:
+                    raise
+                self._recover()
+
+    def close(self):
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
