@@ -71,16 +71,17 @@ def ssm_table(plan, positions, slots: StateSlots) -> np.ndarray:
     return out
 
 
-def attention_groups(plan, n_rep: int):
+def attention_groups(plan, n_rep: int, seq_start=None, seq_ntok=None):
     """Row groups for the tensor-core attention kernel: runs of at most
     128 // n_rep consecutive positions of one sequence (None if every
     sequence contributes a single row, i.e. pure decode)."""
-    ntok = plan.seq_ntok
+    ntok = plan.seq_ntok if plan is not None else seq_ntok
+    starts = plan.seq_start if plan is not None else seq_start
     if len(ntok) == 0 or int(np.max(ntok)) <= 1:
         return None
     ppg = max(1, 128 // n_rep)
     r0, npos = [], []
-    for st, n in zip(plan.seq_start, ntok):
+    for st, n in zip(starts, ntok):
         for o in range(0, int(n), ppg):
             r0.append(int(st) + o)
             npos.append(min(ppg, int(n) - o))

@@ -1,9 +1,14 @@
-"""Multi-GPU arm of bench.py: Llama-3.3-70B pipeline-split over N ranks
-(torchrun, one process per GPU, NCCL p2p between stages).
+"""Multi-GPU arm of bench.py for dense models: Llama-3.3-70B pipeline-split
+over N / tp stages (torchrun, one process per GPU, NCCL p2p between stages),
+tensor-parallel inside each stage when tp > 1, run by the wave-pipelined
+engine (parallel/async_pipeline.py).
 
-Weak scaling: 32 sequences per stage in flight (global batch 32*N), cut into
-N micro-batches.  Device time is CUDA events around exactly K engine steps
-on every rank (barrier + synchronize on both sides), reduced with MAX.
+Weak scaling: `batch` sequences per stage -- one wave of `batch` sequences per
+stage, global batch batch * stages.  Device time: CUDA events on every rank
+around exactly K rounds (K wave steps per wave) with barrier + synchronize on
+both sides, reduced with MAX; the same rounds run through the public API
+(requests in, sampled tokens out), so the host wall time (MAX over ranks) is
+the end-to-end figure.
 """
 from __future__ import annotations
 
@@ -23,12 +28,19 @@ def _log(rank, msg):
         print(f"[bench-pp {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
 
 
+def _max(v: float, dev) -> float:
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def pipeline_bench(args):
     from bench import BASELINE_70B_TOKS, ClockSampler
     from ..engine import EngineConfig, SamplingParams
     from ..models.config import preset
     from ..models.weights import RandomSource
-    from .pipeline import PipelineEngine, init_distributed
+    from .async_pipeline import AsyncPipelineEngine
+    from .pipeline import init_distributed
 
     init_distributed("nccl", timeout_s=600)
     rank, world = dist.get_rank(), dist.get_world_size()
@@ -37,100 +49,103 @@ def pipeline_bench(args):
     if args.layers:
         cfg = cfg.scaled(n_layers=args.layers)
     tp = getattr(args, "tp", 1) or 1
-    n_stages = world // tp
-    B = args.batch * n_stages
+    S = world // tp
+    Bw = args.batch                     # sequences per wave (= per stage)
     P, G = args.prompt, args.gen
-    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=B, max_step_tokens=P,
-                        prefill_chunk=P, kv_pages=B * ((P + G + 64 + 15) // 16) + 64)
+    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=Bw * S, max_step_tokens=P,
+                        prefill_chunk=P, kv_pages=S * Bw * ((P + G + 64 + 15) // 16) + 64)
     t0 = time.time()
-    eng = PipelineEngine(cfg, ecfg, lambda: RandomSource(cfg, seed=1234, on_device=True), dev,
-                         micro_batches=n_stages, tp=tp)
+    eng = AsyncPipelineEngine(cfg, ecfg, lambda: RandomSource(cfg, seed=1234, on_device=True),
+                              dev, tp=tp)
     torch.cuda.synchronize()
     dist.barrier()
-    _log(rank, f"stages {eng.bounds}, init {time.time() - t0:.1f}s")
+    _log(rank, f"stages {eng.bounds} x tp{tp}, waves {eng.V}, init {time.time() - t0:.1f}s")
     rng = np.random.default_rng(0)
     sp = SamplingParams(max_tokens=G, ignore_eos=True)
 
-    def run_until(cond):
-        while True:
-            flag = torch.tensor([1 if (rank != 0 or cond()) else 0], dtype=torch.int32, device=dev)
-            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-            if not flag.item():
-                return
-            eng.step()
-
-    # ---- TTFT: one prompt alone, through the public API
+    # ---- TTFT: one prompt alone through the public API
     ttfts = []
-    for r in range(args.ttft_reps + 1):
+    for _ in range(args.ttft_reps + 1):
         torch.cuda.synchronize()
         dist.barrier()
         t = time.perf_counter()
-        rid = eng.add_request(rng.integers(0, cfg.vocab, P).tolist(),
-                              SamplingParams(max_tokens=1, ignore_eos=True)) if rank == 0 else None
-        run_until(lambda: len(eng.output(rid)) == 0)
-        ttfts.append((time.perf_counter() - t) * 1e3)
         if rank == 0:
-            eng.sched.release(rid)
+            rid = eng.add_request(rng.integers(0, cfg.vocab, P).tolist(),
+                                  SamplingParams(max_tokens=1, ignore_eos=True))
+            eng.run(stop_when=lambda: len(eng.output(rid)) > 0)
+            eng.release(rid)
+        else:
+            eng.run()
+        torch.cuda.synchronize()
+        ttfts.append(_max((time.perf_counter() - t) * 1e3, dev))
     _log(rank, f"ttft (ms) {[round(x, 1) for x in ttfts]}")
 
     def decode(batch):
         rids = []
         if rank == 0:
-            rids = [eng.add_request(rng.integers(0, cfg.vocab, P).tolist(), sp) for _ in range(batch)]
+            rids = [eng.add_request(rng.integers(0, cfg.vocab, P).tolist(), sp)
+                    for _ in range(batch * S)]
         t_pf = time.time()
-        run_until(lambda: eng.sched.num_waiting > 0 or any(len(eng.output(x)) == 0 for x in rids))
-        _log(rank, f"batch {batch}: prefill {time.time() - t_pf:.1f}s")
-        for _ in range(args.warmup):
-            eng.step()
+        eng.run(stop_when=(lambda: all(len(eng.output(x)) > 0 for x in rids)) if rank == 0 else None)
+        _log(rank, f"batch {batch}/wave: prefill {time.time() - t_pf:.1f}s")
+        if rank == 0:
+            target = eng.retired + args.warmup * S
+            eng.run(stop_when=lambda: eng.retired >= target)
+        else:
+            eng.run()
         torch.cuda.synchronize()
         dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(0) as cs:
+        with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as cs:
             t = time.perf_counter()
             a.record()
-            for _ in range(args.steps):
-                eng.step()
+            if rank == 0:
+                target = eng.retired + args.steps * S
+                eng.run(stop_when=lambda: eng.retired >= target)
+            else:
+                eng.run()
             b.record()
             torch.cuda.synchronize()
             wall = time.perf_counter() - t
-        dist.barrier()
-        ms = torch.tensor([a.elapsed_time(b)], device=dev)
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        wl = torch.tensor([wall], device=dev)
-        dist.all_reduce(wl, op=dist.ReduceOp.MAX)
+        ms = _max(a.elapsed_time(b), dev)
+        wall = _max(wall, dev)
         if rank == 0:
             for x in rids:
-                eng.sched.abort(x)
-                eng.sched.release(x)
-        return float(ms.item()), float(wl.item()), cs.summary()
+                eng.abort(x)
+                eng.release(x)
+            eng.run()  # retire the aborted sequences (no work left: returns at once)
+        else:
+            eng.run()
+        return ms, wall, cs.summary()
 
-    ms_b, wall_b, clocks = decode(B)
+    ms_b, wall_b, clocks = decode(Bw)
     ms_1, wall_1, _ = decode(1)
-    value = B * args.steps / (ms_b / 1e3)
-    # every rank runs its stage's forward once per micro-batch
-    launches = torch.tensor([eng.model.decode_launches() * eng.micro * args.steps], device=dev)
+    tokens = args.steps * S * Bw
+    value = tokens / (ms_b / 1e3)
+    launches = torch.tensor([eng.model.decode_launches() * args.steps * S], device=dev)
     dist.all_reduce(launches)
     if rank == 0:
         line = {
-            "metric": f"decode tok/s at batch {args.batch} per stage (aggregate), Llama-3.3-70B Q4_K",
+            "metric": f"decode tok/s at batch {Bw} per stage (aggregate), Llama-3.3-70B Q4_K",
             "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_b / args.steps, 4),
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": round(value / BASELINE_70B_TOKS, 2),
             "dtype": "fp16 activations, fp32 accumulate, Q4_K weights",
             "data": "synthetic uniform-random token ids; random-init Q4_K weights (llama-3.3-70b architecture)",
-            "config": {"model": cfg.name, "layers": cfg.n_layers, "global_batch": B, "seq_len": P,
-                       "gen_len": G,
-                       "parallelism": f"pp{n_stages}" + (f"xtp{tp}" if tp > 1 else ""),
-                       "stages": eng.bounds, "micro_batches": eng.micro,
+            "config": {"model": cfg.name, "layers": cfg.n_layers, "global_batch": Bw * S,
+                       "seq_len": P, "gen_len": G,
+                       "parallelism": f"pp{S}" + (f"xtp{tp}" if tp > 1 else ""),
+                       "stages": eng.bounds, "waves": eng.V,
+                       "step": "one round = every wave advances one token",
                        "tp": "fused: GEMM epilogue pushes partials over NVLink" if tp > 1 else None,
                        "kv": "paged fp16, 16-token pages",
                        "l2": "no flush: weights streamed per step >> 126 MB L2"},
-            "decode_tok_s_batch1": round(args.steps / (ms_1 / 1e3), 2),
+            "decode_tok_s_batch1": round(args.steps * S / (ms_1 / 1e3), 2),
             "ttft_p50_ms": round(statistics.median(ttfts[1:]), 2), "ttft_prompt_tokens": P,
-            "e2e": {"value": round(B * args.steps / wall_b, 2), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(4 * (4 + eng.max_pages) * B + 12),
-                    "d2h_bytes_per_step": 4 * B},
+            "e2e": {"value": round(tokens / wall_b, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(S * 4 * (4 + eng.max_pages + 3) * Bw + 32 * S),
+                    "d2h_bytes_per_step": 4 * Bw * S},
             "gpu_launches": int(launches.item()),
             "clocks": clocks,
         }
@@ -138,4 +153,6 @@ def pipeline_bench(args):
             line["invalid"] = "layer count overridden (debug)"
         print(json.dumps(line), flush=True)
     dist.barrier()
+    if eng.tpg is not None:
+        eng.tpg.close()
     dist.destroy_process_group()

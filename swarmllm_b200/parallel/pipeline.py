@@ -34,7 +34,7 @@ import torch
 import torch.distributed as dist
 
 from ..engine.engine import EngineConfig
-from ..engine.runner import plan_arrays
+from ..engine.runner import attention_groups, plan_arrays
 from ..engine.sampling import DeviceSampler, SamplingParams, sample_host
 from ..models.config import ModelConfig
 from ..models.llama import StepBatch
@@ -204,6 +204,12 @@ class PipelineEngine:
             t = lambda a, dt=torch.int32: torch.as_tensor(np.ascontiguousarray(a), dtype=dt, device=dev)
             batch = StepBatch(t(tokens[r]), t(positions[r]), t(slots[r]), t(bt[r]), t(seq_lens[r]),
                               t(samp_rows, torch.int64), self.ecfg.max_model_len)
+            if self.gpu:
+                grp = attention_groups(None, self.cfg.n_heads // self.cfg.n_kv_heads,
+                                       np.asarray(seq_start[mb.seqs]) - r.start,
+                                       np.asarray(seq_ntok[mb.seqs]))
+                if grp is not None:
+                    batch.groups = (t(grp[0]), t(grp[1]), grp[2])
             h_in = None
             if not self.first:
                 h_in = torch.empty(rows, H, dtype=self.comm_dtype, device=dev)

@@ -76,3 +76,66 @@ def test_stage_bounds():
     sizes = [b[i + 1] - b[i] for i in range(8)]
     assert max(sizes) - min(sizes) <= 2
     assert stage_bounds(2, 2) == [0, 1, 2]
+
+
+def _async_worker(rank, world, port, q):
+    import os
+    import torch
+    import torch.distributed as dist
+    torch.set_num_threads(1)
+    from swarmllm_b200.engine.engine import EngineConfig
+    from swarmllm_b200.engine.sampling import SamplingParams
+    from swarmllm_b200.models.config import tiny_llama
+    from swarmllm_b200.models.weights import RandomSource
+    from swarmllm_b200.parallel.async_pipeline import AsyncPipelineEngine
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = tiny_llama().scaled(n_layers=3)
+    ecfg = EngineConfig(max_model_len=128, max_running=6, max_step_tokens=64, prefill_chunk=16,
+                        prefix_cache=False)
+    eng = AsyncPipelineEngine(cfg, ecfg, lambda: RandomSource(cfg, seed=5), "cpu")
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, cfg.vocab, n).tolist() for n in (5, 30, 12, 21, 9)]
+    out = eng.generate(prompts, SamplingParams(max_tokens=9, ignore_eos=True))
+    if rank == 0:
+        q.put(out)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_async_waves_match_single_process(world):
+    """Wave-pipelined split (independent waves, plan travelling with the
+    activations, chunked prefill) == one process, token for token."""
+    import multiprocessing as mp
+    import socket
+    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from swarmllm_b200.models.config import tiny_llama
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = tiny_llama().scaled(n_layers=3)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, cfg.vocab, n).tolist() for n in (5, 30, 12, 21, 9)]
+    ref = LLMEngine.from_config(cfg, "cpu", EngineConfig(max_model_len=128, max_running=6,
+                                                         max_step_tokens=64, prefill_chunk=16,
+                                                         prefix_cache=False),
+                                source=RandomSource(cfg, seed=5))
+    want = [o.token_ids for o in ref.generate(prompts, SamplingParams(max_tokens=9,
+                                                                      ignore_eos=True))]
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_async_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        got = q.get(timeout=240)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert got == want
