@@ -325,6 +325,32 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                                   out.data_ptr<float>(), cur_stream());
     TORCH_CHECK(rc == 0, "ssm_conv_silu failed: rc=", rc);
   });
+  m.def("lora_delta", [](Tensor x, Tensor ids, Tensor A, Tensor B, Tensor scale, Tensor u,
+                         Tensor delta) {
+    // x [T, K] fp16, ids [T] int32, A [M, R, K] fp16, B [M, rows, R] fp16, scale [M] fp32,
+    // u >= [T, R] fp32 scratch, delta [T, rows] fp32 (out)
+    CHECK_DT(x, at::kHalf); CHECK_DT(ids, at::kInt); CHECK_DT(A, at::kHalf); CHECK_DT(B, at::kHalf);
+    CHECK_DT(scale, at::kFloat); CHECK_DT(u, at::kFloat); CHECK_DT(delta, at::kFloat);
+    CHECK_CONTIG(A); CHECK_CONTIG(B); CHECK_CONTIG(delta);
+    const int T = (int)x.size(0), K = (int)x.size(1), R = (int)A.size(1), rows = (int)B.size(1);
+    TORCH_CHECK(A.size(2) == K && B.size(2) == R && u.numel() >= (int64_t)T * R &&
+                delta.size(0) >= T && delta.size(1) == rows, "lora shapes");
+    const at::cuda::CUDAGuard guard(x.device());
+    TORCH_CHECK(launch_lora(reinterpret_cast<const __half*>(x.data_ptr()), (int)x.stride(0), K,
+                            ids.data_ptr<int32_t>(), T,
+                            reinterpret_cast<const __half*>(A.data_ptr()),
+                            reinterpret_cast<const __half*>(B.data_ptr()), scale.data_ptr<float>(),
+                            R, rows, u.data_ptr<float>(), delta.data_ptr<float>(), cur_stream()) == 0,
+                "lora launch failed");
+  });
+  m.def("gemm_with_add", [](const GemmResult& g, Tensor add) {
+    CHECK_DT(add, at::kFloat);
+    TORCH_CHECK(add.size(-1) == g.g.rows && add.stride(-1) == 1, "add must be [T, rows]");
+    GemmResult r = g;
+    r.g.add = add.data_ptr<float>();
+    r.g.add_stride = (int)add.stride(0);
+    return r;
+  });
   m.def("tree_rank", [](Tensor logits, int64_t k, Tensor ids, Tensor logp, Tensor ws) {
     // ws: float32 scratch of at least rows * S * (2k + 2) elements (tree_rank_ws_floats)
     CHECK_DT(logits, at::kFloat); CHECK_DT(ids, at::kInt); CHECK_DT(logp, at::kFloat);

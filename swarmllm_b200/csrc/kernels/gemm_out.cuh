@@ -33,17 +33,20 @@ struct GemmOut {
   int seg_max;    // unused; kept so the struct layout stays fixed
   int n_src;      // ranks whose partials are summed (0 or 1: just this one)
   long long src_stride;
+  const float* add;  // optional dense [T][add_stride] term added on read (LoRA deltas)
+  int add_stride;
 
 #ifdef __CUDACC__
   __device__ __forceinline__ float get(int t, int r) const {
-    if (mode == 0) return ws[(size_t)t * rows + r];
+    const float extra = add ? add[(size_t)t * add_stride + r] : 0.f;
+    if (mode == 0) return ws[(size_t)t * rows + r] + extra;
     const int rt = r >> 7, rr = r & 127;
     const int nt = t / tok_tile, tt = t - nt * tok_tile;
     const int tile = rt * n_tok_tiles + nt;
     const long u0 = (long)tile * ksb;
     const int c0 = (int)(u0 / upc);
     const int c1 = (int)((u0 + ksb - 1) / upc);
-    float acc = 0.f;
+    float acc = extra;
     const int ns = n_src > 1 ? n_src : 1;
     for (int s = 0; s < ns; ++s) {
       const float* w = ws + (size_t)s * src_stride;

@@ -151,3 +151,8 @@ int launch_tree_rank(const float* logits, int rows, int V, int stride, int k, fl
 // (ctl[slot] + 1); records code/where in status on timeout.
 int launch_flag_wait(const void* flags, int world, int* ctl, int slot, int* status, int code,
                      cudaStream_t s);
+
+// ---- LoRA (lora.cu) -----------------------------------------------------------
+int launch_lora(const __half* x, int x_stride, int K, const int32_t* ids, int T, const __half* A,
+                const __half* B, const float* scale, int R, int rows, float* u, float* delta,
+                cudaStream_t s);

@@ -40,6 +40,8 @@ class EngineConfig:
     prefix_cache: bool = True
     cuda_graphs: bool = True
     graph_sizes: tuple = (1, 2, 4, 8, 16, 32, 64)
+    max_loras: int = 0              # LoRA adapter slots (0: LoRA off)
+    max_lora_rank: int = 64
 
 
 @dataclass
@@ -63,6 +65,12 @@ class LLMEngine:
             # recurrent state cannot be rebuilt from cached KV pages
             ecfg.prefix_cache = False
         n_kv_layers = getattr(model, "n_kv_layers", model.hi - model.lo)
+        self.lora_of: dict[int, int] = {}
+        self.lora_names: list[str] = []
+        if ecfg.max_loras and self.device.type == "cuda":
+            model.enable_lora(ecfg.max_loras, ecfg.max_lora_rank)
+        elif ecfg.max_loras:
+            model.lora_adapters = []
         if self.device.type == "cuda":
             pages = ecfg.kv_pages or self._auto_pages()
             # one extra page: the trash page that graph padding rows write to
@@ -75,6 +83,7 @@ class LLMEngine:
             self.runner = GpuRunner(model, self.kv, ecfg.max_step_tokens, ecfg.max_running,
                                     ecfg.max_model_len, ecfg.graph_sizes, ecfg.cuda_graphs,
                                     trash_page=pages)
+            self.runner.lora_of = self.lora_of if ecfg.max_loras else None
             if ecfg.cuda_graphs:
                 self.runner.capture_graphs()
         else:
@@ -85,6 +94,7 @@ class LLMEngine:
                 self.kv.add_linear_state(lin[0], ecfg.max_running + 1, *lin[1:])
             self.bm = N.BlockManager(pages, ps, ecfg.prefix_cache)
             self.runner = CpuRunner(model, self.kv, ecfg.max_model_len, ecfg.max_running)
+            self.runner.lora_of = self.lora_of if ecfg.max_loras else None
         self.sched = N.Scheduler(self.bm, ecfg.max_step_tokens, ecfg.max_running, ecfg.prefill_chunk)
         self.params: dict[int, SamplingParams] = {}
         self.traces: dict[int, RequestTrace] = {}
@@ -130,10 +140,30 @@ class LLMEngine:
         return int(max(64, min(budget // per_page, need)))
 
     # ------------------------------------------------------------------ API
+    def load_lora(self, adapter, name: str | None = None) -> str:
+        """Register a LoRA adapter (a LoraAdapter or a LoRA GGUF path) for
+        requests to select by name."""
+        from ..models.lora import LoraAdapter
+        if isinstance(adapter, str):
+            adapter = LoraAdapter.from_gguf(adapter, name)
+        if name:
+            adapter.name = name
+        if getattr(self.model, "lora", None) is not None:
+            self.model.lora.add(adapter)
+        elif hasattr(self.model, "lora_adapters"):
+            self.model.lora_adapters.append(adapter)
+        else:
+            raise RuntimeError("engine built without LoRA slots (EngineConfig.max_loras)")
+        if adapter.name not in self.lora_names:
+            self.lora_names.append(adapter.name)
+        return adapter.name
+
     def add_request(self, prompt_ids, params: SamplingParams | None = None,
-                    request_id: int | None = None) -> int:
+                    request_id: int | None = None, lora: str | None = None) -> int:
         params = params or SamplingParams()
         rid = next(self._ids) if request_id is None else request_id
+        if lora is not None:
+            self.lora_of[rid] = self.lora_names.index(lora)
         eos = -1 if params.ignore_eos else params.eos_token_id
         self.sched.add_request(rid, [int(t) for t in prompt_ids], int(params.max_tokens), int(eos))
         self.params[rid] = params
@@ -203,6 +233,7 @@ class LLMEngine:
     def release(self, rid: int):
         self.sched.release(rid)
         self._free_state(rid)
+        self.lora_of.pop(rid, None)
         self.params.pop(rid, None)
         self.prompt_len.pop(rid, None)
 

@@ -71,6 +71,13 @@ def ssm_table(plan, positions, slots: StateSlots) -> np.ndarray:
     return out
 
 
+def lora_rows(plan, lora_of: dict) -> np.ndarray:
+    """int32 [N] adapter index of each token row (-1: none)."""
+    per_seq = np.array([lora_of.get(int(s), -1) for s in plan.seq_ids], np.int32)
+    rs = np.asarray(plan.row_seq)
+    return per_seq[rs] if len(rs) else np.zeros(0, np.int32)
+
+
 def attention_groups(plan, n_rep: int, seq_start=None, seq_ntok=None):
     """Row groups for the tensor-core attention kernel: runs of at most
     128 // n_rep consecutive positions of one sequence (None if every
@@ -116,6 +123,9 @@ class GpuRunner:
         self.graph_sizes = sorted(s for s in graph_sizes if s <= min(max_tokens, max_seqs))
         self.use_graphs = use_graphs
         self.graphs: dict[int, tuple] = {}
+        self.lora_of = None
+        self.d_lora = torch.full((mt,), -1, dtype=torch.int32, device=dev)
+        self.h_lora = torch.full((mt,), -1, dtype=torch.int32).pin_memory()
         self.slots = None
         if getattr(model, "n_lin_layers", 0):
             ms = max(max_seqs, max(graph_sizes))
@@ -174,7 +184,20 @@ class GpuRunner:
                       self.d_lens[:M], self.d_samp[:S], self.max_model_len)
         if self.slots is not None:
             b.ssm_seqs = self.d_ssm[:n_seqs]
+        if self.lora_of is not None:
+            b.lora_ids = self.d_lora[:M]
         return b
+
+    def _upload_lora(self, plan, pad_to: int = 0):
+        if self.lora_of is None:
+            return
+        ids = lora_rows(plan, self.lora_of)
+        n = len(ids)
+        m = max(n, pad_to)
+        self.h_lora[:n] = torch.from_numpy(ids)
+        self.h_lora[n:m] = -1
+        self.d_lora[:m].copy_(self.h_lora[:m], non_blocking=True)
+        self.h2d_bytes += 4 * m
 
     # ------------------------------------------------------------------ graphs
     def capture_graphs(self):
@@ -203,6 +226,7 @@ class GpuRunner:
         self.d_lens[:B] = 1
         self.d_bt[:B] = self.trash_page
         self.d_samp[:B] = torch.arange(B, device=self.device)
+        self.d_lora[:B] = -1
         if self.slots is not None:
             self.d_ssm[:B, 0] = torch.arange(1 << 30, (1 << 30) + B, device=self.device,
                                              dtype=torch.int32)
@@ -225,12 +249,14 @@ class GpuRunner:
             self._upload(tokens, positions, slots, bt_rows, seq_lens, sample_rows, pad_to=B)
             if table is not None:
                 self._upload_ssm(table, pad_to=B)
+            self._upload_lora(plan, pad_to=B)
             g, logits, out = self.graphs[B]
             g.replay()
             res = out[:S]
         else:
             M, _ = self._upload(tokens, positions, slots, bt_rows, seq_lens, sample_rows)
             ns = self._upload_ssm(table) if table is not None else 0
+            self._upload_lora(plan)
             b = self._batch(M, S, ns)
             if table is not None and len(table):
                 b.ssm_max_rows = int(table[:, 1].max())
@@ -263,6 +289,8 @@ class CpuRunner:
                       torch.from_numpy(seq_lens), torch.from_numpy(sample_rows), self.max_model_len)
         if self.slots is not None:
             b.ssm_seqs = torch.from_numpy(ssm_table(plan, positions, self.slots))
+        if getattr(self, "lora_of", None) is not None:
+            b.lora_ids = torch.from_numpy(lora_rows(plan, self.lora_of))
         return self.model.forward(b, self.kv, None, h_in), positions, sample_rows
 
     def run(self, plan, block_manager, params: list[SamplingParams]) -> np.ndarray:

@@ -49,6 +49,7 @@ class StepBatch:
     groups: tuple | None = None             # (row0 int32[G], npos int32[G], positions/group)
     ssm_seqs: torch.Tensor | None = None    # int32 [S, 4] (row0, nrows, state slot, pos0): linear attention
     ssm_max_rows: int = 1                   # host hint: most rows of one sequence in this step
+    lora_ids: torch.Tensor | None = None    # int32 [N] adapter index per row (-1: none)
 
 
 def _f32(t: torch.Tensor, qt: int, shape) -> torch.Tensor:
@@ -73,6 +74,7 @@ class LlamaGPU:
         self.cfg = cfg
         self.ep = ep
         self.tp = tp
+        self.lora = None
         W = tp.world if tp else 1
         tr = tp.rank if tp else 0
         assert cfg.n_heads % W == 0 and cfg.n_kv_heads % W == 0 and cfg.ffn % W == 0
@@ -261,6 +263,26 @@ class LlamaGPU:
             r = max(r, (2 * c.ssm_k_heads + c.ssm_v_heads) * c.ssm_head_dim)
         return r
 
+    def enable_lora(self, max_adapters: int = 4, max_rank: int = 64):
+        """Allocate adapter tables (before contexts / CUDA graphs are made)."""
+        from .lora import LoraSet
+        assert self.tp is None, "LoRA on tensor-parallel shards is not supported"
+        self.lora = LoraSet(self, max_adapters, max_rank)
+        return self.lora
+
+    def _lora(self, j: int, group: str, x, g, ctx, b):
+        """Add the per-row adapter deltas of target `group` to GEMM result g."""
+        if self.lora is None or b.lora_ids is None:
+            return g
+        t = self.lora.tables.get((j, group))
+        if t is None:
+            return g
+        A, B, S, _ = t
+        T, rows = x.shape[0], B.shape[1]
+        delta = ctx.lora_delta[: T * rows].view(T, rows)
+        C().lora_delta(x, b.lora_ids, A, B, S, ctx.lora_u, delta)
+        return C().gemm_with_add(g, delta)
+
     def _row_parallel(self, lin, x, ctx):
         if self.tp is None:
             return lin(x, ctx.gemm)
@@ -330,7 +352,7 @@ class LlamaGPU:
                 C().epi_residual_rmsnorm(g, h, None, L.ffn_norm, x, cfg.rms_eps)
             else:
                 li = self.kv_off + L.kv_idx
-                g = L.wqkv(x, ctx.gemm)
+                g = self._lora(j, "qkv", x, L.wqkv(x, ctx.gemm), ctx, b)
                 gate = ctx.gate[:N] if L.gated else None
                 C().epi_rope_kv(g, L.qkv_bias, b.positions, b.slots, self.inv_freq, nq, nkv, d,
                                 cfg.rot_dim, cfg.rope_neox, self.attn_factor, q, kv.k(li),
@@ -341,7 +363,7 @@ class LlamaGPU:
                                 num_sms=ctx.gemm.num_sms, groups=b.groups)
                 if gate is not None:
                     C().mul_f16(ao, gate)
-                g = self._row_parallel(L.wo, ao, ctx)
+                g = self._lora(j, "o", ao, self._row_parallel(L.wo, ao, ctx), ctx, b)
                 C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
             if j + 1 < len(self.layers):
                 nxt_w, nxt_out = self.layers[j + 1].attn_norm, x
@@ -366,9 +388,9 @@ class LlamaGPU:
                 else:
                     moe_experts(x, L.experts, ctx.moe, h, nxt_w, nxt_out, cfg.rms_eps, sh, shg)
                 continue
-            g = L.wgu(x, ctx.gemm)
+            g = self._lora(j, "gu", x, L.wgu(x, ctx.gemm), ctx, b)
             C().epi_swiglu(g, None, self.ffn_loc, 0, False, 0.0, 0.0, act)
-            g = self._row_parallel(L.wdown, act, ctx)
+            g = self._lora(j, "down", act, self._row_parallel(L.wdown, act, ctx), ctx, b)
             C().epi_residual_rmsnorm(g, h, None, nxt_w if nxt_w is not None else ctx.dummy_norm,
                                      nxt_out, cfg.rms_eps)
         if not self.last:
@@ -418,6 +440,11 @@ class GpuForwardContext:
                                        device=dev)
             self.ssm_out = torch.zeros(max_tokens, nv * dh, dtype=torch.float16, device=dev)
             self.ssm_oraw = torch.zeros(max_tokens, nv * dh, dtype=torch.float32, device=dev)
+        if model.lora is not None:
+            rows = max(t[1].shape[1] for t in model.lora.tables.values())
+            R = max(t[0].shape[1] for t in model.lora.tables.values())
+            self.lora_delta = torch.zeros(max_tokens * rows, dtype=torch.float32, device=dev)
+            self.lora_u = torch.zeros(max_tokens * R, dtype=torch.float32, device=dev)
         self.moe = None
         if cfg.n_experts:
             ex = next(L.experts for L in model.layers if L.experts is not None)
@@ -537,6 +564,24 @@ class LlamaCPU:
             out[..., 1:rd:2] = b * c + a * s
         return out
 
+    def _lora_cpu(self, layer: int, suffix: str, x, y, b):
+        """y += scale * B (A x) for the rows that carry an adapter using this weight."""
+        ads = getattr(self, "lora_adapters", None)
+        if not ads or b.lora_ids is None:
+            return y
+        base = f"blk.{layer}.{suffix}.weight"
+        ids = b.lora_ids.long()
+        for a, ad in enumerate(ads):
+            if base not in ad.tensors:
+                continue
+            rows = (ids == a).nonzero().flatten()
+            if len(rows) == 0:
+                continue
+            A_, B_ = (torch.from_numpy(t).to(y.dtype) for t in ad.tensors[base])
+            y = y.clone()
+            y[rows] += ad.scale(base) * ((x[rows] @ A_.T) @ B_.T)
+        return y
+
     def _act(self, g, u):
         cfg = self.cfg
         if not cfg.swiglu_limit:
@@ -545,10 +590,15 @@ class LlamaCPU:
         u = torch.clamp(u, -cfg.swiglu_limit, cfg.swiglu_limit)
         return g * torch.sigmoid(cfg.swiglu_alpha * g) * (u + 1)
 
-    def _ffn(self, L, x):
+    def _ffn(self, L, x, layer: int = -1, b=None):
         if L.moe:
             return self._moe(x, L)
-        return (torch.nn.functional.silu(x @ L.wg.T) * (x @ L.wu.T)) @ L.wd.T
+        if b is None:
+            return (torch.nn.functional.silu(x @ L.wg.T) * (x @ L.wu.T)) @ L.wd.T
+        gg = self._lora_cpu(layer, "ffn_gate", x, x @ L.wg.T, b)
+        uu = self._lora_cpu(layer, "ffn_up", x, x @ L.wu.T, b)
+        act = torch.nn.functional.silu(gg) * uu
+        return self._lora_cpu(layer, "ffn_down", act, act @ L.wd.T, b)
 
     def _deltanet(self, L, x, b, kv):
         """Gated DeltaNet (sequential recurrence, the definition the GPU
@@ -636,9 +686,10 @@ class LlamaCPU:
                 h = h + self._ffn(L, x)
                 continue
             li = self.kv_off + L.kv_idx
-            q = x @ L.wq.T
-            k = x @ L.wk.T
-            v = x @ L.wv.T
+            layer = self.lo + j
+            q = self._lora_cpu(layer, "attn_q", x, x @ L.wq.T, b)
+            k = self._lora_cpu(layer, "attn_k", x, x @ L.wk.T, b)
+            v = self._lora_cpu(layer, "attn_v", x, x @ L.wv.T, b)
             gate = None
             if cfg.attn_output_gate:
                 qg = q.view(N, nq, 2 * d)
@@ -681,12 +732,12 @@ class LlamaCPU:
             a = att.view(N, nq * d)
             if gate is not None:
                 a = a * gate
-            o = a @ L.wo.T
+            o = self._lora_cpu(layer, "attn_output", a, a @ L.wo.T, b)
             if L.bo is not None:
                 o = o + L.bo
             h = h + o
             x = self._norm(h, L.ffn_norm)
-            h = h + self._ffn(L, x)
+            h = h + self._ffn(L, x, layer, b)
         if not self.last:
             return h
         x = self._norm(h[b.sample_rows.long()], self.out_norm)
