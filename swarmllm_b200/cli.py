@@ -1,6 +1,6 @@
 """Command line: ``python -m swarmllm_b200 <command>``.
 
-  serve     OpenAI/Anthropic-compatible HTTP server on :8800 (reference: `swarmllm run`)
+  serve     OpenAI/Anthropic/Responses/MCP HTTP server on :8800 (reference: `swarmllm run`)
   generate  one-shot generation from token ids or text
   bench     single-GPU tokens/s over a preset (reference: `swarmllm bench`)
   info      model / GGUF summary
@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 import time
 
@@ -28,10 +29,17 @@ def _engine(args):
     ecfg = load_engine_config(args.config)
     if args.max_model_len:
         ecfg.max_model_len = args.max_model_len
+    loras = [x.split("=", 1) for x in getattr(args, "lora", None) or []]
+    if loras:
+        ecfg.max_loras = max(ecfg.max_loras, len(loras))
     dev = args.device or ("cuda:0" if torch.cuda.is_available() else "cpu")
     if args.gguf:
-        return LLMEngine.from_gguf(args.gguf, dev, ecfg)
-    return LLMEngine.from_config(preset(args.model), dev, ecfg, seed=args.seed)
+        eng = LLMEngine.from_gguf(args.gguf, dev, ecfg)
+    else:
+        eng = LLMEngine.from_config(preset(args.model), dev, ecfg, seed=args.seed)
+    for name, path in loras:
+        eng.load_lora(path, name)
+    return eng
 
 
 def _tokenizer(args, eng):
@@ -55,14 +63,24 @@ def main(argv=None):
         s.add_argument("--config", default=None)
         s.add_argument("--seed", type=int, default=0)
         s.add_argument("--max-model-len", type=int, default=0)
+        s.add_argument("--lora", action="append", default=[], metavar="NAME=PATH",
+                       help="LoRA adapter GGUF; requests select it with model NAME")
         if name == "serve":
             s.add_argument("--host", default="0.0.0.0")
             s.add_argument("--port", type=int, default=8800)
+            s.add_argument("--api-key", default=os.environ.get("SWARMLLM_API_KEY"),
+                           help="require this key (Bearer or x-api-key); default: open")
+            s.add_argument("--cors-origin", action="append", default=[],
+                           help="extra browser origin allowed besides localhost")
+            s.add_argument("--rpm", type=int, default=0, help="requests a minute per client (0: off)")
+            s.add_argument("--response-store", default=None,
+                           help="SQLite file for stored /v1/responses (default: in memory)")
         if name == "generate":
             s.add_argument("--prompt", default="Hello")
             s.add_argument("--ids", default=None, help="comma-separated token ids")
             s.add_argument("--max-tokens", type=int, default=32)
             s.add_argument("--temperature", type=float, default=0.0)
+            s.add_argument("--adapter", default=None, help="name of a --lora adapter to generate with")
         if name == "bench":
             s.add_argument("--batch", type=int, default=8)
             s.add_argument("--prompt-len", type=int, default=512)
@@ -97,16 +115,21 @@ def main(argv=None):
         from .serve.api import serve
         tok, tpl = _tokenizer(args, eng)
         serve(eng, tok, eng.cfg.name, args.host, args.port, arch=eng.cfg.arch, chat_template=tpl,
-              max_model_len=eng.ecfg.max_model_len)
+              max_model_len=eng.ecfg.max_model_len, api_key=args.api_key,
+              cors_origins=tuple(args.cors_origin), rpm=args.rpm, store_path=args.response_store)
         return
     from .engine.sampling import SamplingParams
     if args.cmd == "generate":
         tok, _ = _tokenizer(args, eng)
         ids = [int(x) for x in args.ids.split(",")] if args.ids else tok.encode(args.prompt)
-        out = eng.generate([ids], SamplingParams(max_tokens=args.max_tokens,
-                                                 temperature=args.temperature))[0]
-        print(json.dumps({"token_ids": out.token_ids, "text": tok.decode(out.token_ids),
-                          "ttft_ms": out.trace.ttft * 1e3 if out.trace and out.trace.ttft else None}))
+        sp = SamplingParams(max_tokens=args.max_tokens, temperature=args.temperature)
+        rid = eng.add_request(ids, sp, lora=args.adapter) if args.adapter else eng.add_request(ids, sp)
+        toks = []
+        while eng.has_work():
+            toks += [t for r, t, _ in eng.step() if r == rid]
+        tr = eng.traces.get(rid)
+        print(json.dumps({"token_ids": toks, "text": tok.decode(toks),
+                          "ttft_ms": tr.ttft * 1e3 if tr is not None and tr.ttft else None}))
         return
     if args.cmd == "bench":
         import numpy as np

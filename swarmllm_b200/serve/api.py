@@ -1,13 +1,23 @@
-"""OpenAI- and Anthropic-compatible HTTP API on port 8800.
+"""OpenAI-, Anthropic- and MCP-compatible HTTP API on port 8800.
 
-Routes (reference: src/api/server.rs:239-559, src/api/openai/mod.rs:319,
+Routes (reference: src/api/server.rs:239-330, src/api/openai/mod.rs:319,
 src/api/openai/streaming.rs:1431, src/api/anthropic/):
-  POST /v1/chat/completions    (stream=true -> SSE chunks, data: [DONE])
+  POST /v1/chat/completions    (stream=true -> SSE chunks, data: [DONE]); tools,
+                               tool_choice, response_format
   POST /v1/completions
-  POST /v1/messages            (Anthropic Messages; stream -> typed SSE events)
+  POST /v1/messages            (Anthropic Messages; tools -> tool_use blocks;
+                               stream -> typed SSE events)
+  POST /v1/responses, GET/DELETE /v1/responses/{id}, POST .../cancel,
+  GET .../input_items          (OpenAI Responses API: serve/responses.py)
+  POST/GET/DELETE /mcp         (Model Context Protocol server: serve/mcp.py)
   POST /v1/embeddings          (mean-pooled, L2-normalised input embeddings)
-  GET  /v1/models
-  GET  /health, /health/ready, /metrics (Prometheus), /api/status
+  GET  /v1/models              (the base model and every loaded LoRA adapter)
+  GET  /health, /health/ready, /metrics (Prometheus), /api/status, /v1/status
+  WS   /api/admin/ws           (status feed, one JSON message a second)
+
+Auth, CORS, rate limits, security headers and the body-size cap are one ASGI
+middleware (serve/middleware.py).  A request selects a LoRA adapter by naming
+it as the model ("adapter" or "base:adapter").
 
 The engine is single-threaded: ``AsyncEngine`` runs ``step()`` in a worker
 thread, takes new requests from a queue between steps and hands each token
@@ -23,13 +33,15 @@ import queue
 import threading
 import time
 import uuid
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
-from fastapi import Request  # module level: route annotations are resolved from globals
+from fastapi import Request, WebSocket  # module level: route annotations resolve from globals
 
 from ..engine.sampling import SamplingParams
 from ..utils.metrics import Metrics
 from .chat_template import render
+from .tools import (ToolSpec, content_prefix_len, format_tool_prompt, parse_tool_calls,
+                    tool_choice_forbids, tools_from_anthropic, tools_from_openai)
 
 
 @dataclass
@@ -39,6 +51,7 @@ class _Sub:
     params: SamplingParams
     q: asyncio.Queue
     loop: asyncio.AbstractEventLoop
+    lora: str | None = None
 
 
 class AsyncEngine:
@@ -55,10 +68,11 @@ class AsyncEngine:
         self._t = threading.Thread(target=self._run, daemon=True, name="engine")
         self._t.start()
 
-    def submit(self, prompt_ids, params: SamplingParams) -> tuple[int, asyncio.Queue]:
+    def submit(self, prompt_ids, params: SamplingParams,
+               lora: str | None = None) -> tuple[int, asyncio.Queue]:
         rid = next(self._ids)
         q: asyncio.Queue = asyncio.Queue()
-        self._in.put(_Sub(rid, list(prompt_ids), params, q, asyncio.get_running_loop()))
+        self._in.put(_Sub(rid, list(prompt_ids), params, q, asyncio.get_running_loop(), lora))
         self._wake.set()
         return rid, q
 
@@ -80,7 +94,8 @@ class AsyncEngine:
                 except queue.Empty:
                     break
                 try:
-                    eng.add_request(s.prompt, s.params, request_id=s.rid)
+                    kw = {"lora": s.lora} if s.lora else {}
+                    eng.add_request(s.prompt, s.params, request_id=s.rid, **kw)
                     self._subs[s.rid] = s
                     self.metrics.requests_started()
                 except Exception as e:  # bad request: report and drop
@@ -129,196 +144,388 @@ class AsyncEngine:
             s.loop.call_soon_threadsafe(s.q.put_nowait, ("done", reason, tr))
 
 
-def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "llama",
-               chat_template: str | None = None, max_model_len: int = 4096):
-    from fastapi import FastAPI, HTTPException
-    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+class ApiError(Exception):
+    def __init__(self, status: int, message: str, kind: str = "invalid_request_error"):
+        super().__init__(message)
+        self.status, self.message, self.kind = status, message, kind
 
-    app = FastAPI(title="swarmllm_b200")
-    eos = getattr(tokenizer, "eos_id", -1)
 
-    def params_from(body: dict, n_prompt: int) -> SamplingParams:
-        mt = body.get("max_tokens", body.get("max_completion_tokens"))
+@dataclass
+class Result:
+    """One finished generation."""
+    text: str = ""
+    calls: list = field(default_factory=list)
+    finish: str = "stop"            # stop | length | tool_calls
+    n_prompt: int = 0
+    n_out: int = 0
+    trace: object = None
+    rest: str = ""                  # content not yet streamed when the result arrived
+
+
+class Serving:
+    """What every route shares: the engine, tokenizer, templates and the one
+    generation path (tools, response_format, LoRA selection, stop strings)."""
+
+    def __init__(self, aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "llama",
+                 chat_template: str | None = None, max_model_len: int = 4096):
+        self.ae, self.tok, self.model_name = aengine, tokenizer, model_name
+        self.arch, self.template, self.max_model_len = arch, chat_template, max_model_len
+        self.eos = getattr(tokenizer, "eos_id", -1)
+        self.started = time.time()
+
+    # ---------------------------------------------------------------- request parsing
+    def lora_of(self, body: dict) -> str | None:
+        """The LoRA adapter a request's "model" names (None: the base model)."""
+        names = getattr(self.ae.engine, "lora_names", None) or []
+        m = body.get("model")
+        if not m or not names or m == self.model_name:
+            return None
+        name = m.split(":", 1)[1] if ":" in m and m.split(":", 1)[0] == self.model_name else m
+        if name in names:
+            return name
+        return None
+
+    def models(self) -> list[str]:
+        return [self.model_name] + [f"{self.model_name}:{n}" for n in
+                                    getattr(self.ae.engine, "lora_names", None) or []]
+
+    def params(self, body: dict, n_prompt: int) -> SamplingParams:
+        mt = body.get("max_tokens", body.get("max_completion_tokens", body.get("max_output_tokens")))
         if mt is None:
-            mt = max(1, min(1024, max_model_len - n_prompt))
-        if n_prompt + int(mt) > max_model_len:
-            raise HTTPException(400, f"prompt ({n_prompt}) + max_tokens ({mt}) exceeds the "
-                                     f"context window ({max_model_len})")
-        return SamplingParams(max_tokens=int(mt), temperature=float(body.get("temperature", 1.0)),
-                              top_p=float(body.get("top_p", 1.0)), top_k=int(body.get("top_k", 0) or 0),
-                              seed=int(body.get("seed", 0) or 0), eos_token_id=int(eos),
+            mt = max(1, min(1024, self.max_model_len - n_prompt))
+        if int(mt) < 1:
+            raise ApiError(400, "max_tokens must be at least 1")
+        if n_prompt + int(mt) > self.max_model_len:
+            raise ApiError(400, f"prompt ({n_prompt}) + max_tokens ({mt}) exceeds the "
+                                f"context window ({self.max_model_len})")
+        t = body.get("temperature")
+        return SamplingParams(max_tokens=int(mt), temperature=float(1.0 if t is None else t),
+                              top_p=float(body.get("top_p", 1.0) or 1.0),
+                              top_k=int(body.get("top_k", 0) or 0),
+                              seed=int(body.get("seed", 0) or 0), eos_token_id=int(self.eos),
                               ignore_eos=bool(body.get("ignore_eos", False)))
 
-    def stops_of(body: dict) -> list[str]:
+    @staticmethod
+    def stops(body: dict) -> list[str]:
         st = body.get("stop") or body.get("stop_sequences") or []
         return [st] if isinstance(st, str) else list(st)
 
-    async def generate(prompt_ids, sp: SamplingParams, stops: list[str]):
-        """Async generator of (text_delta, finish_reason|None, trace|None)."""
-        rid, q = aengine.submit(prompt_ids, sp)
+    def prepare(self, messages: list[dict], tools: list[ToolSpec] | None = None, tool_choice=None,
+                response_format: dict | None = None) -> tuple[list[int], list[ToolSpec]]:
+        """Token ids of the rendered conversation; the tools that stay active."""
+        msgs = [self._flatten(m) for m in messages]
+        extra = []
+        if tools and not tool_choice_forbids(tool_choice):
+            extra.append(format_tool_prompt(tools, tool_choice))
+        else:
+            tools = []
+        if response_format and response_format.get("type") in ("json_object", "json_schema"):
+            s = "Reply with one valid JSON object and nothing else."
+            schema = (response_format.get("json_schema") or {}).get("schema")
+            if schema:
+                s += " It must conform to this JSON schema: " + json.dumps(schema)
+            extra.append(s)
+        if extra:
+            text = "\n\n".join(extra)
+            if msgs and msgs[0]["role"] == "system":
+                msgs[0] = {"role": "system", "content": msgs[0]["content"] + "\n\n" + text}
+            else:
+                msgs.insert(0, {"role": "system", "content": text})
+        ids = self.tok.encode(render(msgs, self.arch, self.template))
+        return ids, tools
+
+    @staticmethod
+    def _flatten(m: dict) -> dict:
+        """One message with plain-text content: assistant tool calls become the
+        JSON shape the tool prompt asks for; tool results become text."""
+        role = m.get("role", "user")
+        c = m.get("content", "")
+        if isinstance(c, list):
+            parts = []
+            for p in c:
+                if not isinstance(p, dict):
+                    continue
+                t = p.get("type")
+                if t in ("text", "input_text", "output_text"):
+                    parts.append(p.get("text", ""))
+                elif t == "tool_use":
+                    parts.append(json.dumps({"tool_calls": [{"name": p.get("name"),
+                                                             "arguments": p.get("input", {})}]}))
+                elif t == "tool_result":
+                    inner = p.get("content", "")
+                    if isinstance(inner, list):
+                        inner = "".join(x.get("text", "") for x in inner if isinstance(x, dict))
+                    parts.append(f"[tool result {p.get('tool_use_id', '')}] {inner}")
+            c = "".join(parts)
+        calls = m.get("tool_calls")
+        if calls:
+            c = (c or "") + json.dumps({"tool_calls": [
+                {"name": (x.get("function") or x).get("name"),
+                 "arguments": _loads_or((x.get("function") or x).get("arguments"))} for x in calls]})
+        if role == "tool":
+            c = f"[tool result {m.get('tool_call_id', '')}] {c}"
+        return {"role": role, "content": c or ""}
+
+    # ---------------------------------------------------------------- generation
+    async def stream(self, ids, sp: SamplingParams, stops: list[str], tools=None,
+                     lora: str | None = None):
+        """Async generator of events:
+             ("text", delta)          content to show now
+             ("done", Result)         at the end (calls parsed, counts, trace)."""
+        rid, q = self.ae.submit(ids, sp, lora)
         toks: list[int] = []
-        emitted = ""
+        text = ""
+        sent = 0
         try:
             while True:
                 msg = await q.get()
                 if msg[0] == "error":
-                    raise HTTPException(500, msg[1])
+                    raise ApiError(500, msg[1], "server_error")
                 if msg[0] == "done":
-                    yield "", ("length" if len(toks) >= sp.max_tokens else "stop"), msg[2]
+                    fin = "length" if len(toks) >= sp.max_tokens else "stop"
+                    yield self._finish(text, sent, tools, fin, len(ids), len(toks), msg[2])
                     return
                 toks.append(msg[1])
-                if msg[1] == eos and not sp.ignore_eos:
+                if msg[1] == self.eos and not sp.ignore_eos:
                     continue
-                text = tokenizer.decode(toks)
-                hit = next((s for s in stops if s in text), None)
-                if hit is not None:
-                    text = text[:text.index(hit)]
-                    delta = text[len(emitted):]
-                    emitted = text
-                    aengine.abort(rid)
-                    yield delta, "stop", None
+                text = self.tok.decode([t for t in toks if t != self.eos or sp.ignore_eos])
+                hit = min((text.index(s) for s in stops if s in text), default=-1)
+                if hit >= 0:
+                    text = text[:hit]
+                    self.ae.abort(rid)
+                    yield self._finish(text, sent, tools, "stop", len(ids), len(toks), None)
                     return
-                delta = text[len(emitted):]
-                emitted = text
-                if delta:
-                    yield delta, None, None
+                safe = content_prefix_len(text) if tools else len(text)
+                if safe > sent:
+                    yield ("text", text[sent:safe])
+                    sent = safe
         except asyncio.CancelledError:
-            aengine.abort(rid)
+            self.ae.abort(rid)
             raise
+
+    @staticmethod
+    def _finish(text, sent, tools, fin, n_prompt, n_out, trace):
+        r = Result(text=text, finish=fin, n_prompt=n_prompt, n_out=n_out, trace=trace)
+        parsed = parse_tool_calls(text, tools) if tools else None
+        if parsed is not None:
+            r.text, r.calls, r.finish = parsed[0], parsed[1], "tool_calls"
+        r.rest = r.text[sent:] if len(r.text) > sent else ""
+        return ("done", r)
+
+    async def run(self, ids, sp, stops, tools=None, lora=None) -> Result:
+        async for ev in self.stream(ids, sp, stops, tools, lora):
+            if ev[0] == "done":
+                return ev[1]
+        raise ApiError(500, "generation ended without a result", "server_error")
+
+
+def _loads_or(v):
+    if isinstance(v, str):
+        try:
+            return json.loads(v)
+        except ValueError:
+            return v
+    return v if v is not None else {}
+
+
+def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "llama",
+               chat_template: str | None = None, max_model_len: int = 4096,
+               api_key: str | None = None, cors_origins=(), rpm: int = 0, port: int = 8800,
+               store_path: str | None = None):
+    from fastapi import FastAPI
+    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+    from . import mcp, responses
+    from .middleware import SecurityMiddleware
+
+    app = FastAPI(title="swarmllm_b200")
+    S = Serving(aengine, tokenizer, model_name, arch, chat_template, max_model_len)
+    app.state.serving = S
+
+    @app.exception_handler(ApiError)
+    async def _api_error(request: Request, e: ApiError):
+        if request.url.path.startswith("/v1/messages"):
+            return JSONResponse({"type": "error", "error": {"type": e.kind, "message": e.message}},
+                                status_code=e.status)
+        return JSONResponse({"error": {"message": e.message, "type": e.kind}}, status_code=e.status)
 
     def headers_of(tr) -> dict:
         return tr.headers() if tr is not None else {}
 
+    async def body_of(request: Request) -> dict:
+        try:
+            body = await request.json()
+        except ValueError:
+            raise ApiError(400, "request body is not valid JSON")
+        if not isinstance(body, dict):
+            raise ApiError(400, "request body must be a JSON object")
+        return body
+
+    def sse(obj) -> str:
+        return f"data: {json.dumps(obj)}\n\n"
+
     # ------------------------------------------------------------------ OpenAI chat
     @app.post("/v1/chat/completions")
     async def chat_completions(request: Request):
-        body = await request.json()
+        body = await body_of(request)
         msgs = body.get("messages")
         if not msgs:
-            raise HTTPException(400, "messages is required")
-        prompt = render(msgs, arch, chat_template)
-        ids = tokenizer.encode(prompt)
-        sp = params_from(body, len(ids))
-        stops = stops_of(body)
+            raise ApiError(400, "messages is required")
+        try:
+            tools = tools_from_openai(body.get("tools"))
+        except ValueError as e:
+            raise ApiError(400, str(e))
+        ids, tools = S.prepare(msgs, tools, body.get("tool_choice"), body.get("response_format"))
+        sp = S.params(body, len(ids))
+        lora = S.lora_of(body)
+        stops = S.stops(body)
         cid = "chatcmpl-" + uuid.uuid4().hex[:24]
         created = int(time.time())
+        model = body.get("model") or model_name
+
+        def chunk(delta, fin=None):
+            return sse({"id": cid, "object": "chat.completion.chunk", "created": created,
+                        "model": model, "choices": [{"index": 0, "delta": delta, "finish_reason": fin}]})
+
         if body.get("stream"):
-            async def sse():
-                first = {"id": cid, "object": "chat.completion.chunk", "created": created,
-                         "model": model_name,
-                         "choices": [{"index": 0, "delta": {"role": "assistant"}, "finish_reason": None}]}
-                yield f"data: {json.dumps(first)}\n\n"
-                n = 0
-                async for delta, fin, tr in generate(ids, sp, stops):
-                    if delta:
-                        n += 1
-                        ch = {"id": cid, "object": "chat.completion.chunk", "created": created,
-                              "model": model_name,
-                              "choices": [{"index": 0, "delta": {"content": delta}, "finish_reason": None}]}
-                        yield f"data: {json.dumps(ch)}\n\n"
-                    if fin:
-                        end = {"id": cid, "object": "chat.completion.chunk", "created": created,
-                               "model": model_name,
-                               "choices": [{"index": 0, "delta": {}, "finish_reason": fin}]}
-                        yield f"data: {json.dumps(end)}\n\n"
+            async def gen():
+                yield chunk({"role": "assistant"})
+                async for ev in S.stream(ids, sp, stops, tools, lora):
+                    if ev[0] == "text":
+                        yield chunk({"content": ev[1]})
+                        continue
+                    r = ev[1]
+                    if r.rest:
+                        yield chunk({"content": r.rest})
+                    if r.calls:
+                        yield chunk({"tool_calls": [dict(c.openai(), index=i)
+                                                    for i, c in enumerate(r.calls)]})
+                    yield chunk({}, r.finish)
+                    if (body.get("stream_options") or {}).get("include_usage"):
+                        yield sse({"id": cid, "object": "chat.completion.chunk", "created": created,
+                                   "model": model, "choices": [],
+                                   "usage": {"prompt_tokens": r.n_prompt, "completion_tokens": r.n_out,
+                                             "total_tokens": r.n_prompt + r.n_out}})
                 yield "data: [DONE]\n\n"
-            return StreamingResponse(sse(), media_type="text/event-stream")
-        text, fin, trace = "", "stop", None
-        async for delta, f, tr in generate(ids, sp, stops):
-            text += delta
-            if f:
-                fin, trace = f, tr
-        n_out = len(tokenizer.encode(text, add_bos=False)) if text else 0
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        r = await S.run(ids, sp, stops, tools, lora)
+        msg = {"role": "assistant", "content": r.text if (r.text or not r.calls) else None}
+        if r.calls:
+            msg["tool_calls"] = [c.openai() for c in r.calls]
         return JSONResponse({
-            "id": cid, "object": "chat.completion", "created": created, "model": model_name,
-            "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
-                         "finish_reason": fin}],
-            "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out,
-                      "total_tokens": len(ids) + n_out}}, headers=headers_of(trace))
+            "id": cid, "object": "chat.completion", "created": created, "model": model,
+            "choices": [{"index": 0, "message": msg, "finish_reason": r.finish}],
+            "usage": {"prompt_tokens": r.n_prompt, "completion_tokens": r.n_out,
+                      "total_tokens": r.n_prompt + r.n_out}}, headers=headers_of(r.trace))
 
     # ------------------------------------------------------------------ OpenAI completions
     @app.post("/v1/completions")
     async def completions(request: Request):
-        body = await request.json()
+        body = await body_of(request)
         p = body.get("prompt", "")
         ids = list(p) if isinstance(p, list) and p and isinstance(p[0], int) else tokenizer.encode(
             p if isinstance(p, str) else "".join(p))
-        sp = params_from(body, len(ids))
+        sp = S.params(body, len(ids))
+        lora = S.lora_of(body)
         cid = "cmpl-" + uuid.uuid4().hex[:24]
         if body.get("stream"):
-            async def sse():
-                async for delta, fin, tr in generate(ids, sp, stops_of(body)):
-                    ch = {"id": cid, "object": "text_completion", "model": model_name,
-                          "choices": [{"index": 0, "text": delta, "finish_reason": fin}]}
-                    yield f"data: {json.dumps(ch)}\n\n"
+            async def gen():
+                async for ev in S.stream(ids, sp, S.stops(body), None, lora):
+                    if ev[0] == "text":
+                        ch = {"id": cid, "object": "text_completion", "model": model_name,
+                              "choices": [{"index": 0, "text": ev[1], "finish_reason": None}]}
+                    else:
+                        ch = {"id": cid, "object": "text_completion", "model": model_name,
+                              "choices": [{"index": 0, "text": ev[1].rest, "finish_reason": ev[1].finish}]}
+                    yield sse(ch)
                 yield "data: [DONE]\n\n"
-            return StreamingResponse(sse(), media_type="text/event-stream")
-        text, fin = "", "stop"
-        async for delta, f, tr in generate(ids, sp, stops_of(body)):
-            text += delta
-            fin = f or fin
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        r = await S.run(ids, sp, S.stops(body), None, lora)
         return {"id": cid, "object": "text_completion", "model": model_name,
-                "choices": [{"index": 0, "text": text, "finish_reason": fin}],
-                "usage": {"prompt_tokens": len(ids)}}
+                "choices": [{"index": 0, "text": r.text, "finish_reason": r.finish}],
+                "usage": {"prompt_tokens": r.n_prompt, "completion_tokens": r.n_out,
+                          "total_tokens": r.n_prompt + r.n_out}}
 
     # ------------------------------------------------------------------ Anthropic messages
     @app.post("/v1/messages")
     async def messages(request: Request):
-        body = await request.json()
+        body = await body_of(request)
         msgs = list(body.get("messages") or [])
+        if not msgs:
+            raise ApiError(400, "messages is required")
         sysmsg = body.get("system")
         if sysmsg:
             msgs = [{"role": "system", "content": sysmsg if isinstance(sysmsg, str) else
                      "".join(b.get("text", "") for b in sysmsg)}] + msgs
-        ids = tokenizer.encode(render(msgs, arch, chat_template))
-        sp = params_from(body, len(ids))
+        ids, tools = S.prepare(msgs, tools_from_anthropic(body.get("tools")), body.get("tool_choice"))
+        sp = S.params(body, len(ids))
+        lora = S.lora_of(body)
         mid = "msg_" + uuid.uuid4().hex[:24]
+        stop_of = {"length": "max_tokens", "tool_calls": "tool_use", "stop": "end_turn"}
         if body.get("stream"):
-            async def sse():
+            async def gen():
                 def ev(kind, data):
                     return f"event: {kind}\ndata: {json.dumps(data)}\n\n"
                 yield ev("message_start", {"type": "message_start", "message": {
-                    "id": mid, "type": "message", "role": "assistant", "model": model_name,
-                    "content": [], "usage": {"input_tokens": len(ids), "output_tokens": 0}}})
-                yield ev("content_block_start", {"type": "content_block_start", "index": 0,
-                                                 "content_block": {"type": "text", "text": ""}})
-                stop = "end_turn"
-                async for delta, fin, tr in generate(ids, sp, stops_of(body)):
+                    "id": mid, "type": "message", "role": "assistant", "model": body.get("model", model_name),
+                    "content": [], "stop_reason": None,
+                    "usage": {"input_tokens": len(ids), "output_tokens": 0}}})
+                opened = False
+                async for e in S.stream(ids, sp, S.stops(body), tools, lora):
+                    delta = e[1] if e[0] == "text" else e[1].rest
                     if delta:
+                        if not opened:
+                            yield ev("content_block_start", {"type": "content_block_start", "index": 0,
+                                                             "content_block": {"type": "text", "text": ""}})
+                            opened = True
                         yield ev("content_block_delta", {"type": "content_block_delta", "index": 0,
                                                          "delta": {"type": "text_delta", "text": delta}})
-                    if fin == "length":
-                        stop = "max_tokens"
-                yield ev("content_block_stop", {"type": "content_block_stop", "index": 0})
-                yield ev("message_delta", {"type": "message_delta", "delta": {"stop_reason": stop}})
+                    if e[0] != "done":
+                        continue
+                    r = e[1]
+                    idx = 0
+                    if opened:
+                        yield ev("content_block_stop", {"type": "content_block_stop", "index": 0})
+                        idx = 1
+                    for c in r.calls:
+                        blk = c.anthropic()
+                        yield ev("content_block_start", {"type": "content_block_start", "index": idx,
+                                                         "content_block": dict(blk, input={})})
+                        yield ev("content_block_delta", {"type": "content_block_delta", "index": idx,
+                                                         "delta": {"type": "input_json_delta",
+                                                                   "partial_json": c.arguments}})
+                        yield ev("content_block_stop", {"type": "content_block_stop", "index": idx})
+                        idx += 1
+                    yield ev("message_delta", {"type": "message_delta",
+                                               "delta": {"stop_reason": stop_of[r.finish], "stop_sequence": None},
+                                               "usage": {"output_tokens": r.n_out}})
                 yield ev("message_stop", {"type": "message_stop"})
-            return StreamingResponse(sse(), media_type="text/event-stream")
-        text, stop = "", "end_turn"
-        async for delta, f, tr in generate(ids, sp, stops_of(body)):
-            text += delta
-            if f == "length":
-                stop = "max_tokens"
-        return {"id": mid, "type": "message", "role": "assistant", "model": model_name,
-                "content": [{"type": "text", "text": text}], "stop_reason": stop,
-                "usage": {"input_tokens": len(ids)}}
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        r = await S.run(ids, sp, S.stops(body), tools, lora)
+        content = ([{"type": "text", "text": r.text}] if r.text or not r.calls else []) + \
+            [c.anthropic() for c in r.calls]
+        return {"id": mid, "type": "message", "role": "assistant", "model": body.get("model", model_name),
+                "content": content, "stop_reason": stop_of[r.finish], "stop_sequence": None,
+                "usage": {"input_tokens": r.n_prompt, "output_tokens": r.n_out}}
 
     # ------------------------------------------------------------------ embeddings
     @app.post("/v1/embeddings")
     async def embeddings(request: Request):
-        body = await request.json()
+        body = await body_of(request)
         inp = body.get("input", "")
         texts = [inp] if isinstance(inp, str) else list(inp)
         out = []
         for i, t in enumerate(texts):
-            vec = aengine.engine.embed_text(tokenizer.encode(t, add_bos=False))
+            ids = list(t) if isinstance(t, list) else tokenizer.encode(t, add_bos=False)
+            vec = aengine.engine.embed_text(ids)
             out.append({"object": "embedding", "index": i, "embedding": vec})
         return {"object": "list", "data": out, "model": model_name}
 
     # ------------------------------------------------------------------ info / health / metrics
     @app.get("/v1/models")
     async def models():
-        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "local",
-                                            "max_model_len": max_model_len}]}
+        return {"object": "list", "data": [{"id": m, "object": "model", "owned_by": "local",
+                                            "max_model_len": max_model_len} for m in S.models()]}
 
     @app.get("/health")
     async def health():
@@ -330,12 +537,22 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
             return JSONResponse({"status": "unavailable"}, status_code=503)
         return {"status": "ready"}
 
+    def status_dict() -> dict:
+        e = aengine.engine
+        return {"model": model_name, "models": S.models(), "running": e.sched.num_running,
+                "waiting": e.sched.num_waiting, "kv_pages_free": e.bm.num_free(),
+                "kv_pages": e.bm.num_pages, "prefix_cache_hit_tokens": e.bm.prefix_hit_tokens,
+                "steps": e.steps, "uptime_s": round(time.time() - S.started, 1),
+                "ready": aengine.ready}
+    S.status = status_dict
+
     @app.get("/api/status")
     async def status():
-        e = aengine.engine
-        return {"model": model_name, "running": e.sched.num_running, "waiting": e.sched.num_waiting,
-                "kv_pages_free": e.bm.num_free(), "kv_pages": e.bm.num_pages,
-                "prefix_cache_hit_tokens": e.bm.prefix_hit_tokens, "steps": e.steps}
+        return status_dict()
+
+    @app.get("/v1/status")
+    async def v1_status():
+        return status_dict()
 
     @app.get("/metrics")
     async def metrics():
@@ -343,13 +560,38 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
         aengine.metrics.set_kv(e.bm.num_free(), e.bm.num_pages)
         return PlainTextResponse(aengine.metrics.render(), media_type="text/plain; version=0.0.4")
 
+    @app.websocket("/api/admin/ws")
+    async def ws_feed(ws: WebSocket):
+        """Dashboard feed: the status dict once a second until the client leaves."""
+        await ws.accept()
+        try:
+            n = int(ws.query_params.get("n", "0") or 0)   # n > 0: stop after n messages
+            i = 0
+            while True:
+                await ws.send_json(dict(status_dict(), type="status", seq=i))
+                i += 1
+                if n and i >= n:
+                    break
+                await asyncio.sleep(1.0)
+        except Exception:
+            pass
+        finally:
+            try:
+                await ws.close()
+            except Exception:
+                pass
+
+    responses.register(app, S, store_path)
+    mcp.register(app, S)
+    app.add_middleware(SecurityMiddleware, api_key=api_key, port=port,
+                       cors_origins=tuple(cors_origins), rpm=rpm)
     return app
 
 
 def serve(engine, tokenizer, model_name: str, host: str = "0.0.0.0", port: int = 8800, **kw):
     import uvicorn
     ae = AsyncEngine(engine)
-    app = create_app(ae, tokenizer, model_name, **kw)
+    app = create_app(ae, tokenizer, model_name, port=port, **kw)
     try:
         uvicorn.run(app, host=host, port=port, log_level="info")
     finally:

@@ -1,0 +1,352 @@
+"""Tool calling, the Responses API, the MCP server and the request guards.
+
+The server logic is tested against a scripted engine whose output text is
+fixed (through the byte tokenizer), so tool-call parsing and the event
+sequences are exact; the real CPU engine is covered by test_api.py."""
+import json
+import time
+import types
+
+import pytest
+
+from swarmllm_b200.serve.tools import (ToolSpec, content_prefix_len, parse_tool_calls,
+                                       tools_from_openai)
+
+WEATHER = ToolSpec("get_weather", "weather", {"type": "object", "properties": {
+    "city": {"type": "string"}, "days": {"type": "integer"}}})
+DATE = ToolSpec("date")
+
+
+@pytest.mark.parametrize("text,want", [
+    ('{"tool_calls": [{"name": "get_weather", "arguments": {"city": "Paris"}}]}',
+     [("get_weather", {"city": "Paris"})]),
+    ('Sure. {"tool_calls": [{"function": {"name": "date", "arguments": "{}"}}]}', [("date", {})]),
+    ('<tool_call>\n{"name": "get_weather", "arguments": {"city": "Oslo"}}\n</tool_call>'
+     '<tool_call>{"name":"date","arguments":{}}</tool_call>',
+     [("get_weather", {"city": "Oslo"}), ("date", {})]),
+    ('<tool_call>\n<function=get_weather>\n<parameter=city>\nRome\n</parameter>\n'
+     '<parameter=days>\n3\n</parameter>\n</function>\n</tool_call>',
+     [("get_weather", {"city": "Rome", "days": 3})]),
+    ('[TOOL_CALLS][{"name": "date", "arguments": {}}]', [("date", {})]),
+    ('[TOOL_CALLS]get_weather[ARGS]{"city": "Kyiv"}', [("get_weather", {"city": "Kyiv"})]),
+    ('functools[{"name": "date", "arguments": {}}]', [("date", {})]),
+    ('<|tool_calls|>[{"name": "date", "arguments": {}}]<|/tool_calls|>', [("date", {})]),
+    ('<|python_tag|>{"name": "get_weather", "parameters": {"city": "Lima"}}',
+     [("get_weather", {"city": "Lima"})]),
+    ('{"name": "get_weather", "parameters": {"city": "Lima"}}', [("get_weather", {"city": "Lima"})]),
+    ('```json\n{"tool_calls": [{"name": "date", "arguments": {}}]}\n```', [("date", {})]),
+    ("The answer is {x} in math.", None),
+    ('{"tool_calls": [{"name": "rm_rf", "arguments": {}}]}', None),     # undeclared tool
+    ('{"tool_calls": [{"name": "date", "argum', None),                   # truncated
+    ('{"name": "get_weather", "parameters": {"type": "object", "properties": {}}}', None),  # echo
+])
+def test_parse_tool_calls(text, want):
+    r = parse_tool_calls(text, [WEATHER, DATE])
+    if want is None:
+        assert r is None
+        return
+    lead, calls = r
+    assert [(c.name, json.loads(c.arguments)) for c in calls] == want
+    assert len({c.id for c in calls}) == len(calls)
+
+
+def test_content_prefix_len_streaming():
+    assert content_prefix_len("Hello world") == 11
+    assert content_prefix_len("Hello <tool") == 6
+    assert content_prefix_len("Hello {") == 6
+    assert content_prefix_len("x [TOOL") == 2
+    assert content_prefix_len("ab`") == 2
+
+
+def test_tools_from_openai_rejects_builtin():
+    with pytest.raises(ValueError):
+        tools_from_openai([{"type": "web_search"}])
+    assert tools_from_openai([{"type": "function", "name": "f"}])[0].name == "f"
+
+
+# --------------------------------------------------------------------------- scripted engine
+class Scripted:
+    """Engine stand-in: every request generates `script` (byte tokens, offset
+    3, then EOS=2), one token per step."""
+
+    def __init__(self, script: str, step_s: float = 0.0):
+        self.script = [b + 3 for b in script.encode()] + [2]
+        self.step_s = step_s
+        self.reqs, self.traces, self.steps = {}, {}, 0
+        self.lora_names = ["ad1"]
+        self.loras = {}
+        self.sched = types.SimpleNamespace(num_running=0, num_waiting=0)
+        self.bm = types.SimpleNamespace(num_free=lambda: 10, num_pages=10, prefix_hit_tokens=0)
+        self.prompts = []
+
+    def add_request(self, ids, sp, request_id, lora=None):
+        self.reqs[request_id] = [0, sp.max_tokens]
+        self.loras[request_id] = lora
+        self.prompts.append(ids)
+
+    def has_work(self):
+        return bool(self.reqs)
+
+    def step(self):
+        time.sleep(self.step_s)
+        self.steps += 1
+        out = []
+        for rid, st in list(self.reqs.items()):
+            tok = self.script[min(st[0], len(self.script) - 1)]
+            st[0] += 1
+            fin = st[0] >= st[1] or tok == 2
+            out.append((rid, tok, fin))
+            if fin:
+                del self.reqs[rid]
+        return out
+
+    def abort(self, rid):
+        self.reqs.pop(rid, None)
+
+    def release(self, rid):
+        pass
+
+
+def _client(script, step_s=0.0, **kw):
+    from fastapi.testclient import TestClient
+
+    from swarmllm_b200.serve.api import AsyncEngine, create_app
+    from swarmllm_b200.serve.tokenizer import ByteTokenizer
+    eng = Scripted(script, step_s)
+    ae = AsyncEngine(eng)
+    app = create_app(ae, ByteTokenizer(512), "m", max_model_len=4096, **kw)
+    return TestClient(app), ae, eng
+
+
+TOOLS = [{"type": "function", "function": {"name": "get_weather", "description": "w",
+                                           "parameters": WEATHER.parameters}}]
+CALL = '{"tool_calls": [{"name": "get_weather", "arguments": {"city": "Paris"}}]}'
+
+
+def test_chat_tool_call_and_stream():
+    c, ae, eng = _client(CALL)
+    with c:
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "w?"}],
+                                                 "tools": TOOLS, "max_tokens": 200})
+        j = r.json()
+        ch = j["choices"][0]
+        assert ch["finish_reason"] == "tool_calls", j
+        tc = ch["message"]["tool_calls"][0]
+        assert tc["function"]["name"] == "get_weather"
+        assert json.loads(tc["function"]["arguments"]) == {"city": "Paris"}
+        assert j["usage"]["completion_tokens"] == len(CALL) + 1
+        # the tool prompt reached the model
+        assert b"get_weather" in bytes(t - 3 for t in eng.prompts[-1] if 3 <= t < 259)
+        with c.stream("POST", "/v1/chat/completions", json={
+                "messages": [{"role": "user", "content": "w?"}], "tools": TOOLS, "stream": True,
+                "max_tokens": 200}) as s:
+            chunks = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: {")]
+        deltas = [x["choices"][0]["delta"] for x in chunks]
+        assert not any(d.get("content") for d in deltas)       # the JSON never leaks as content
+        assert any("tool_calls" in d for d in deltas)
+        assert chunks[-1]["choices"][0]["finish_reason"] == "tool_calls"
+        # tool_choice none: the JSON is plain content
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "w?"}],
+                                                 "tools": TOOLS, "tool_choice": "none", "max_tokens": 200})
+        assert r.json()["choices"][0]["message"]["content"] == CALL
+        # a follow-up turn carrying the call and its result renders
+        r = c.post("/v1/chat/completions", json={"messages": [
+            {"role": "user", "content": "w?"},
+            {"role": "assistant", "content": None, "tool_calls": [tc]},
+            {"role": "tool", "tool_call_id": tc["id"], "content": "sunny"}], "tools": TOOLS,
+            "max_tokens": 200})
+        assert r.status_code == 200
+    ae.shutdown()
+
+
+def test_anthropic_tool_use():
+    c, ae, _ = _client(CALL)
+    with c:
+        r = c.post("/v1/messages", json={"max_tokens": 200, "messages": [{"role": "user", "content": "w"}],
+                                         "tools": [{"name": "get_weather", "input_schema": WEATHER.parameters}]})
+        j = r.json()
+        assert j["stop_reason"] == "tool_use"
+        blk = [b for b in j["content"] if b["type"] == "tool_use"][0]
+        assert blk["name"] == "get_weather" and blk["input"] == {"city": "Paris"}
+        with c.stream("POST", "/v1/messages", json={
+                "max_tokens": 200, "stream": True, "messages": [{"role": "user", "content": "w"}],
+                "tools": [{"name": "get_weather", "input_schema": WEATHER.parameters}]}) as s:
+            evs = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: ")]
+        kinds = [e["type"] for e in evs]
+        assert kinds[0] == "message_start" and kinds[-1] == "message_stop"
+        assert any(e.get("delta", {}).get("type") == "input_json_delta" for e in evs)
+        assert [e for e in evs if e["type"] == "message_delta"][0]["delta"]["stop_reason"] == "tool_use"
+    ae.shutdown()
+
+
+def test_lora_selected_by_model_name():
+    c, ae, eng = _client("hi")
+    with c:
+        c.post("/v1/chat/completions", json={"model": "m:ad1", "max_tokens": 4,
+                                             "messages": [{"role": "user", "content": "x"}]})
+        c.post("/v1/chat/completions", json={"model": "m", "max_tokens": 4,
+                                             "messages": [{"role": "user", "content": "x"}]})
+        assert list(eng.loras.values()) == ["ad1", None]
+        assert [m["id"] for m in c.get("/v1/models").json()["data"]] == ["m", "m:ad1"]
+    ae.shutdown()
+
+
+# --------------------------------------------------------------------------- Responses API
+def test_responses_basic_chain_and_items():
+    c, ae, eng = _client("Hello there")
+    with c:
+        r = c.post("/v1/responses", json={"model": "m", "input": "hi", "instructions": "be nice",
+                                          "max_output_tokens": 64})
+        j = r.json()
+        assert r.status_code == 200 and j["status"] == "completed", j
+        assert j["output"][0]["type"] == "message"
+        assert j["output"][0]["content"][0]["text"] == "Hello there" == j["output_text"]
+        assert j["usage"]["output_tokens"] == len("Hello there") + 1
+        rid = j["id"]
+        assert c.get(f"/v1/responses/{rid}").json()["id"] == rid
+        # chaining: the previous input and output are in the new prompt, its instructions are not
+        r2 = c.post("/v1/responses", json={"input": [{"role": "user", "content": "again"}],
+                                           "previous_response_id": rid, "max_output_tokens": 64})
+        assert r2.status_code == 200
+        prompt = bytes(t - 3 for t in eng.prompts[-1] if 3 <= t < 259).decode()
+        assert "hi" in prompt and "Hello there" in prompt and "again" in prompt
+        assert "be nice" not in prompt
+        items = c.get(f"/v1/responses/{r2.json()['id']}/input_items?order=asc").json()
+        assert items["data"][0]["type"] == "message" and not items["has_more"]
+        # truncation -> incomplete
+        r3 = c.post("/v1/responses", json={"input": "hi", "max_output_tokens": 3}).json()
+        assert r3["status"] == "incomplete" and r3["incomplete_details"]["reason"] == "max_output_tokens"
+        # store=false is not retrievable; delete works once
+        r4 = c.post("/v1/responses", json={"input": "hi", "store": False, "max_output_tokens": 8}).json()
+        assert c.get(f"/v1/responses/{r4['id']}").status_code == 404
+        assert c.delete(f"/v1/responses/{rid}").json()["deleted"] is True
+        assert c.delete(f"/v1/responses/{rid}").status_code == 404
+        assert c.post("/v1/responses", json={"input": "x", "previous_response_id": rid}).status_code == 404
+        assert c.post("/v1/responses", json={"input": "x", "tools": [{"type": "web_search"}]}).status_code == 400
+    ae.shutdown()
+
+
+def test_responses_stream_events_and_function_calls():
+    c, ae, _ = _client(CALL)
+    with c:
+        with c.stream("POST", "/v1/responses", json={"input": "w?", "stream": True, "max_output_tokens": 200,
+                                                     "tools": [{"type": "function", "name": "get_weather",
+                                                                "parameters": WEATHER.parameters}]}) as s:
+            evs = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: ")]
+        kinds = [e["type"] for e in evs]
+        assert kinds[:2] == ["response.created", "response.in_progress"]
+        assert kinds[-1] == "response.completed"
+        assert "response.function_call_arguments.done" in kinds
+        assert [e["sequence_number"] for e in evs] == list(range(1, len(evs) + 1))
+        out = evs[-1]["response"]["output"]
+        assert out[-1]["type"] == "function_call" and json.loads(out[-1]["arguments"]) == {"city": "Paris"}
+        # answer the call with function_call_output in a chained request
+        r = c.post("/v1/responses", json={"previous_response_id": evs[-1]["response"]["id"],
+                                          "max_output_tokens": 200, "input": [
+            {"type": "function_call_output", "call_id": out[-1]["call_id"], "output": "sunny"}]})
+        assert r.status_code == 200
+    ae.shutdown()
+
+
+def test_responses_background_replay_and_cancel():
+    c, ae, _ = _client("abcdefghij" * 5, step_s=0.01)
+    with c:
+        r = c.post("/v1/responses", json={"input": "x", "background": True, "max_output_tokens": 30})
+        assert r.status_code == 202 and r.headers["location"].endswith(r.json()["id"])
+        rid = r.json()["id"]
+        for _ in range(500):
+            j = c.get(f"/v1/responses/{rid}").json()
+            if j["status"] not in ("queued", "in_progress"):
+                break
+            time.sleep(0.01)
+        assert j["status"] == "incomplete" and j["output_text"] == ("abcdefghij" * 3)
+        with c.stream("GET", f"/v1/responses/{rid}?stream=true&starting_after=3") as s:
+            evs = [json.loads(l[6:]) for l in s.iter_lines() if l.startswith("data: ")]
+        assert evs[0]["sequence_number"] == 4 and evs[-1]["type"] == "response.incomplete"
+        # cancel a long run
+        r = c.post("/v1/responses", json={"input": "x", "background": True, "max_output_tokens": 3000})
+        rid = r.json()["id"]
+        time.sleep(0.05)
+        assert c.post(f"/v1/responses/{rid}/cancel").json()["status"] == "cancelled"
+        assert c.get(f"/v1/responses/{rid}").json()["status"] == "cancelled"
+    ae.shutdown()
+
+
+# --------------------------------------------------------------------------- MCP
+def _rpc(c, method, params=None, rid=1):
+    return c.post("/mcp", json={"jsonrpc": "2.0", "id": rid, "method": method, "params": params or {}})
+
+
+def test_mcp_protocol():
+    c, ae, _ = _client("ok")
+    with c:
+        j = _rpc(c, "initialize", {"protocolVersion": "2025-06-18"}).json()
+        assert j["result"]["protocolVersion"] == "2025-06-18"
+        assert _rpc(c, "initialize", {"protocolVersion": "1999-01-01"}).json()["result"]["protocolVersion"] == "2025-11-25"
+        r = c.post("/mcp", json={"jsonrpc": "2.0", "method": "notifications/initialized"})
+        assert r.status_code == 202 and r.content == b""
+        names = [t["name"] for t in _rpc(c, "tools/list").json()["result"]["tools"]]
+        assert {"chat", "models", "compare", "batch_prompts", "node_info"} <= set(names)
+        res = _rpc(c, "tools/call", {"name": "chat", "arguments": {"prompt": "hi", "max_tokens": 8}}).json()
+        assert res["result"]["content"][0]["text"] == "ok" and not res["result"]["isError"]
+        res = _rpc(c, "tools/call", {"name": "batch_prompts", "arguments": {"tasks": [
+            {"id": "a", "prompt": "1"}, {"id": "b", "prompt": "2", "model": "m:ad1"}]}}).json()
+        assert [x["id"] for x in res["result"]["structuredContent"]["results"]] == ["a", "b"]
+        res = _rpc(c, "tools/call", {"name": "compare", "arguments": {"prompt": "1"}}).json()
+        assert len(res["result"]["structuredContent"]["results"]) == 2
+        res = _rpc(c, "tools/call", {"name": "chat", "arguments": {"prompt": "1", "model": "nope"}}).json()
+        assert res["result"]["isError"] is True
+        assert _rpc(c, "tools/call", {"name": "nope"}).json()["error"]["code"] == -32602
+        ls = _rpc(c, "resources/list").json()["result"]["resources"]
+        assert {x["uri"] for x in ls} == {"swarmllm://status", "swarmllm://models", "swarmllm://peers"}
+        rd = _rpc(c, "resources/read", {"uri": "swarmllm://models"}).json()["result"]["contents"][0]
+        assert json.loads(rd["text"])["models"] == ["m", "m:ad1"]
+        assert _rpc(c, "resources/read", {"uri": "x://y"}).json()["error"]["code"] == -32002
+        assert _rpc(c, "bogus/method").json()["error"]["code"] == -32601
+        bad = c.post("/mcp", content=b"{not json", headers={"content-type": "application/json"})
+        assert bad.status_code == 400 and bad.json()["error"]["code"] == -32700 and bad.json()["id"] is None
+        bad = c.post("/mcp", json=[{"jsonrpc": "2.0", "id": 1, "method": "ping"}])
+        assert bad.json()["error"]["code"] == -32600
+        assert c.get("/mcp").status_code == 405 and c.delete("/mcp").status_code == 200
+    ae.shutdown()
+
+
+# --------------------------------------------------------------------------- guards
+def test_auth_cors_rate_limit_body_cap():
+    c, ae, _ = _client("ok", api_key="sekrit", rpm=4, cors_origins=("https://app.example",))
+    with c:
+        assert c.get("/health").status_code == 200                      # exempt
+        r = c.get("/v1/models")
+        assert r.status_code == 401 and r.headers["x-content-type-options"] == "nosniff"
+        assert c.get("/v1/models", headers={"Authorization": "Bearer wrong"}).status_code == 401
+        assert c.get("/v1/models", headers={"authorization": "bearer sekrit"}).status_code == 200
+        assert c.get("/v1/models", headers={"x-api-key": "sekrit"}).status_code == 200
+        r = c.get("/v1/models", headers={"x-api-key": "sekrit"})   # 5th in the minute, failures count
+        assert r.status_code == 429 and int(r.headers["retry-after"]) >= 1
+        pre = c.options("/v1/chat/completions", headers={"Origin": "https://app.example",
+                                                         "Access-Control-Request-Method": "POST"})
+        assert pre.status_code == 204 and pre.headers["access-control-allow-origin"] == "https://app.example"
+        assert c.options("/v1/models", headers={"Origin": "https://evil.example"}).status_code == 403
+        big = c.post("/api/status", content=b"x", headers={"x-api-key": "sekrit",
+                                                          "content-length": str(64 << 20)})
+        assert big.status_code == 413
+    ae.shutdown()
+
+
+def test_rate_limiter_refill_and_isolation():
+    from swarmllm_b200.serve.middleware import RateLimiter
+    now = [0.0]
+    rl = RateLimiter(60, clock=lambda: now[0])
+    assert all(rl.acquire("a") == 0 for _ in range(60))
+    assert rl.acquire("a") > 0 and rl.acquire("b") == 0
+    now[0] += 1.0                      # one token a second at 60 rpm
+    assert rl.acquire("a") == 0 and rl.acquire("a") > 0
+
+
+def test_status_websocket_feed():
+    c, ae, _ = _client("ok", api_key="k")
+    with c:
+        with c.websocket_connect("/api/admin/ws?n=2&token=k") as ws:
+            a, b = ws.receive_json(), ws.receive_json()
+        assert a["type"] == "status" and (a["seq"], b["seq"]) == (0, 1)
+    ae.shutdown()
