@@ -404,6 +404,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("epi_copy", &epi_copy);
   m.def("qmatmul_simt", &qmatmul_simt);
   m.def("q4k_tc_plan", &q4k_tc_plan_py);
+  m.def("q4k_plan_max_ctas", [](int64_t T, int64_t num_sms) { return q4k_plan_max_ctas((int)T, (int)num_sms); });
+  m.def("q4k_gemv_max_t", []() { return q4k_gemv_max_t(); });
+  m.def("q4k_gemv_occupancy", [](int64_t T) { return q4k_gemv_occupancy((int)T); });
   m.def("qgemm_q4k_tc", &qgemm_q4k_tc);
   m.def("qgemm_q4k_tc_tp", &qgemm_q4k_tc_tp);
   m.def("flag_wait", [](int64_t flags, int64_t world, Tensor ctl, int64_t slot, Tensor status,

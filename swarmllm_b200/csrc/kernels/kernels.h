@@ -36,6 +36,18 @@ void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
 int launch_qmatmul_simt(const void* w, int type, int rows, int K, const __half* x, int x_stride,
                         int T, float* out, int out_stride, cudaStream_t s);
 int q4k_tc_tok_tile(int T);
+// Decode at <= kQGemvMaxT tokens runs the CUDA-core GEMV (qgemv_q4k.cu) with
+// q4k_gemv_ctas_per_sm(T) CTAs per SM; the plan below accounts for it.
+constexpr int kQGemvMaxT = 2;
+constexpr int q4k_gemv_ctas_per_sm(int T) { return T == 1 ? 5 : 4; }
+int q4k_gemv_max_t();          // kQGemvMaxT unless SWARMLLM_QGEMV_MAX_T overrides (0 = off)
+int q4k_plan_max_ctas(int T, int num_sms);
+int q4k_gemv_occupancy(int T);  // resident GEMV CTAs per SM (diagnostics)
+int launch_qgemv_q4k(const void* w_packed, int rows, int K, const __half* x, int x_stride, int T,
+                     float* ws, int ksb, long total_units, int upc, int ctas, int* status,
+                     const unsigned long long* peer_ws, int n_peers, int* sig_ctl,
+                     const unsigned long long* sig_bases, long long sig_flag_off, int sig_rank,
+                     cudaStream_t s);
 void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* ksb,
                  long* total_units, int* upc, int* n_ctas, size_t* ws_floats);
 int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, int x_stride,

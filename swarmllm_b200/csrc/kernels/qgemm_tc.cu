@@ -49,7 +49,7 @@ constexpr int kTmemCols = 512;
 // of TMEM A stages and its own W stages (the stage counts are multiples of the
 // warpgroup count), so a stage is always re-used by the warpgroup that used it
 // last and no parity wait can run two phases ahead.
-template <int N, bool HALVES = false>
+template <int N>
 struct QCfg {
   // Dequantizer warpgroups take units round-robin; each owns one "unit stage":
   // 128 TMEM columns of A (K=256 fp16) plus the unit's activation tile in smem,
@@ -80,7 +80,6 @@ struct QGemmArgs {
   float* ws;
   int* status;
   unsigned long long* trace;  // debug: per-unit event timestamps of CTA 0 (null = off)
-  uint32_t poll_ns;           // back-off between failed barrier polls (0 = none)
   // Tensor parallelism: when n_peers > 0 the partial tiles go to every rank's
   // receive buffer (peer_ws[o], over NVLink) instead of `ws`, and the CTA that
   // finishes last raises flag word sig_bases[o] + sig_flag_off + 4 * sig_rank.
@@ -99,66 +98,10 @@ struct QGemmArgs {
         globaltimer();                                                                 \
   } while (0)
 
-// Bounded waits with an optional back-off between failed polls: waiting warps
-// then take fewer issue slots from the dequantizer warps.
-SW_DEVICE bool qwait(uint64_t* bar, uint32_t parity, int* status, int code, int d0, int d1,
-                     uint32_t ns) {
-  if (ns == 0) return mbar_wait(bar, parity, status, code, d0, d1);
-  const uint32_t addr = smem_u32(bar);
-  if (mbar_try_wait(addr, parity)) return true;
-  const unsigned long long t0 = globaltimer();
-  while (true) {
-    for (int i = 0; i < 16; ++i) {
-      __nanosleep(ns);
-      if (mbar_try_wait(addr, parity)) return true;
-    }
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
-      if (status && atomicCAS(status, 0, code) == 0) {
-        status[1] = blockIdx.x;
-        status[2] = d0;
-        status[3] = d1;
-        status[4] = (int)parity;
-        status[5] = threadIdx.x;
-      }
-      return false;
-    }
-  }
-}
-
-SW_DEVICE bool qwait_warp(uint64_t* bar, uint32_t parity, int* status, int code, int d0, int d1,
-                          uint32_t ns) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = qwait(bar, parity, status, code, d0, d1, ns) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  __syncwarp();
-  return ok != 0;
-}
-
-// Sub-blocks [4h, 4h+4) of a superblock into the unit's TMEM columns.
-SW_DEVICE void dq_half(const uint4 (&q)[8], const float* sc, const float* mb, uint32_t taddr,
-                       int h) {
-  const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int sub = 4 * h + j;
-    const __half2 S = __float2half2_rn(sc[sub]), S16 = __float2half2_rn(sc[sub] * 0.0625f);
-    const __half2 MB = __float2half2_rn(-mb[sub]);
-    uint32_t cols[16];
-#pragma unroll
-    for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[4 * sub + w4], S, S16, MB, cols + 4 * w4);
-    tmem_st_x16(taddr + sub * 16, cols);
-  }
-}
-
-// HALVES: each A/X stage has one `ready` barrier per 128-K half (the X
-// producer's two boxes of that half complete on it, the dequantizer warps
-// arrive after their half), so the MMA issuer starts the first 8 MMAs of a
-// unit while the second half is still being dequantized.
-template <int N, bool HALVES>
+template <int N>
 __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
     qgemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap x_map, QGemmArgs a) {
   using C = QCfg<N>;
-  constexpr int RH = HALVES ? 2 : 1;  // ready barriers per stage
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -167,8 +110,8 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_smem + C::W_BYTES);
   uint64_t* w_full = bars;                 // W stage loaded (tx)
   uint64_t* w_empty = w_full + C::W_ST;    // W stage read by its warpgroup (4 warps)
-  uint64_t* ready = w_empty + C::W_ST;     // unit (or half): A in TMEM (4 warps) + X in smem (tx)
-  uint64_t* empty = ready + RH * C::U;     // unit consumed by the MMAs (commit)
+  uint64_t* ready = w_empty + C::W_ST;     // unit: A in TMEM (4 warps) + X in smem (producer + tx)
+  uint64_t* empty = ready + C::U;          // unit consumed by the MMAs (commit)
   uint64_t* d_full = empty + C::U;
   uint64_t* d_empty = d_full + 1;
   uint64_t* done_bar = d_empty + 1;
@@ -181,8 +124,7 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::W_ST; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
-    for (int i = 0; i < RH * C::U; ++i) mbar_init(&ready[i], 5);
-    for (int i = 0; i < C::U; ++i) mbar_init(&empty[i], 1);
+    for (int i = 0; i < C::U; ++i) { mbar_init(&ready[i], 5); mbar_init(&empty[i], 1); }
     mbar_init(d_full, 1);
     mbar_init(d_empty, 4);
     mbar_init(done_bar, 1);
@@ -207,7 +149,7 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
       for (int i = 0; i < n_units && ok; ++i, (++sb == a.ksb) ? (sb = 0, ++tile) : 0) {
         const int rt = tile / a.n_tok_tiles;
         const int wsi = i % C::W_ST;
-        if (!(ok = qwait(&w_empty[wsi], ((i / C::W_ST) & 1) ^ 1, a.status, 11, i, 0, a.poll_ns))) break;
+        if (!(ok = mbar_wait(&w_empty[wsi], ((i / C::W_ST) & 1) ^ 1, a.status, 11, i, 0))) break;
         QTRACE(a.trace, i, 0);
         mbar_arrive_expect_tx(&w_full[wsi], kWStageBytes);
         bulk_load(w_smem + wsi * kWStageBytes,
@@ -227,23 +169,17 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
       for (int i = 0; i < n_units && ok; ++i, (++sb == a.ksb) ? (sb = 0, ++tile) : 0) {
         const int nt = tile % a.n_tok_tiles;
         const int s = i % C::U;
-        if (!(ok = qwait(&empty[s], ((i / C::U) & 1) ^ 1, a.status, 12, i, 0, a.poll_ns))) break;
+        if (!(ok = mbar_wait(&empty[s], ((i / C::U) & 1) ^ 1, a.status, 12, i, 0))) break;
+        mbar_arrive_expect_tx(&ready[s], C::X_UNIT_BYTES);
         uint8_t* dst = x_smem + s * C::X_UNIT_BYTES;
 #pragma unroll
-        for (int h = 0; h < RH; ++h) {
-          uint64_t* rb = &ready[RH * s + h];
-          mbar_arrive_expect_tx(rb, C::X_UNIT_BYTES / RH);
-#pragma unroll
-          for (int c = h * (4 / RH); c < (h + 1) * (4 / RH); ++c)
-            tma_load_2d(dst + c * (N * 128), &x_map, sb * 256 + c * 64, nt * N, rb);
-        }
+        for (int c = 0; c < 4; ++c) tma_load_2d(dst + c * (N * 128), &x_map, sb * 256 + c * 64, nt * N, &ready[s]);
         QTRACE(a.trace, i, 1);
         ++issued;
       }
       if (!ok)
         for (int i = max(0, issued - C::U); i < issued; ++i)
-          for (int h = 0; h < RH; ++h)
-            mbar_wait(&ready[RH * (i % C::U) + h], (i / C::U) & 1, nullptr, 0);
+          mbar_wait(&ready[i % C::U], (i / C::U) & 1, nullptr, 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -265,20 +201,16 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
           if (!(ok = mbar_wait(d_empty, (seg - 1) & 1, a.status, 21, i, seg))) break;
         }
         const int s = i % C::U;
+        if (!(ok = mbar_wait(&ready[s], (i / C::U) & 1, a.status, 22, i, 0))) break;
+        QTRACE(a.trace, i, 5);
+        tc_fence_after();
         const uint64_t xd = xdesc[0] + (uint64_t)((s * C::X_UNIT_BYTES) >> 4);
         const uint32_t ab = tmem_base + C::A_COL + s * 128;
+        umma_f16_ts(tmem_base, ab, xd, idesc, first ? 0u : 1u);
 #pragma unroll
-        for (int h = 0; h < RH; ++h) {
-          if (!(ok = mbar_wait(&ready[RH * s + h], (i / C::U) & 1, a.status, 22, i, h))) break;
-          QTRACE(a.trace, i, 5);
-          tc_fence_after();
-#pragma unroll
-          for (int kk = h * (16 / RH); kk < (h + 1) * (16 / RH); ++kk)
-            umma_f16_ts(tmem_base, ab + kk * 8,
-                        xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4), idesc,
-                        (first && kk == 0) ? 0u : 1u);
-        }
-        if (!ok) break;
+        for (int kk = 1; kk < 16; ++kk)
+          umma_f16_ts(tmem_base, ab + kk * 8, xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4),
+                      idesc, 1u);
         umma_commit(&empty[s]);
         if (last) {
           umma_commit(d_full);
@@ -304,7 +236,7 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
       const bool last = (i == n_units - 1) || (sb == a.ksb - 1);
       if ((i % C::DQ) == g) {
         const int wsi = i % C::W_ST;
-        if (!(ok = qwait_warp(&w_full[wsi], (i / C::W_ST) & 1, a.status, 31, i, 0, a.poll_ns))) break;
+        if (!(ok = mbar_wait_warp(&w_full[wsi], (i / C::W_ST) & 1, a.status, 31, i, 0))) break;
         if (lane == 0) QTRACE(tr, i, 2);
         const uint4* src = reinterpret_cast<const uint4*>(w_smem + wsi * kWStageBytes +
                                                            row * kQ4kRowBytes);
@@ -317,26 +249,14 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
         float sc_f[8], mb_f[8];
         q4k_decode_scales(hdr, sc_f, mb_f);
         const int s = i % C::U;
-        if (!(ok = qwait_warp(&empty[s], ((i / C::U) & 1) ^ 1, a.status, 32, i, 0, a.poll_ns))) break;
+        if (!(ok = mbar_wait_warp(&empty[s], ((i / C::U) & 1) ^ 1, a.status, 32, i, 0))) break;
         if (lane == 0) QTRACE(tr, i, 7);
         tc_fence_after();
-        const uint32_t taddr = tmem_base + lane_off + C::A_COL + s * 128;
-        if constexpr (HALVES) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            dq_half(q, sc_f, mb_f, taddr, h);
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ready[2 * s + h]);
-          }
-        } else {
-          dq_unit(q, sc_f, mb_f, taddr);
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ready[s]);
-        }
+        dq_unit(q, sc_f, mb_f, tmem_base + lane_off + C::A_COL + s * 128);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[s]);
         if (lane == 0) QTRACE(tr, i, 3);
       }
       if (last) {
@@ -473,7 +393,23 @@ int q4k_tc_tok_tile(int T) {
   return 128;  // N=128 already runs the tensor core at full rate (48..69 clk per K=16 MMA)
 }
 
+static int q_env(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v ? atoi(v) : dflt;
+}
+static const int g_gemv_max_t = [] {
+  const int v = q_env("SWARMLLM_QGEMV_MAX_T", kQGemvMaxT);
+  return v < 0 ? 0 : (v > kQGemvMaxT ? kQGemvMaxT : v);
+}();
+int q4k_gemv_max_t() { return g_gemv_max_t; }
+
+int q4k_plan_max_ctas(int T, int num_sms) {
+  return T <= g_gemv_max_t ? q4k_gemv_ctas_per_sm(T) * num_sms : num_sms;
+}
+
 // Work decomposition shared by the launcher, the workspace sizing and GemmOut.
+// At <= q4k_gemv_max_t() tokens the units go to the GEMV's CTAs instead (same
+// partial-slot format, token tile 16).
 void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* ksb,
                  long* total_units, int* upc, int* n_ctas, size_t* ws_floats) {
   const int N = q4k_tc_tok_tile(T);
@@ -481,7 +417,8 @@ void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_
   const int kb = K / 256;
   const int tiles = ((rows + 127) / 128) * ntt;
   const long total = (long)tiles * kb;
-  const int u = (int)((total + num_sms - 1) / num_sms);
+  const int max_ctas = q4k_plan_max_ctas(T, num_sms);
+  const int u = (int)((total + max_ctas - 1) / max_ctas);
   const int ctas = (int)((total + u - 1) / u);
   *tok_tile = N;
   *n_tok_tiles = ntt;
@@ -492,33 +429,20 @@ void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_
   *ws_floats = (size_t)(tiles + ctas) * N * 128;
 }
 
-template <int N, bool HALVES>
-static int launch_nh(const CUtensorMap& map, const QGemmArgs& a, int n_ctas, cudaStream_t s) {
+template <int N>
+static int launch_n(const CUtensorMap& map, const QGemmArgs& a, int n_ctas, cudaStream_t s) {
   using C = QCfg<N>;
   static bool attr_set = false;
   if (!attr_set) {
-    if (cudaFuncSetAttribute(qgemm_q4k_tc_kernel<N, HALVES>,
+    if (cudaFuncSetAttribute(qgemm_q4k_tc_kernel<N>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
       return -3;
     attr_set = true;
   }
-  qgemm_q4k_tc_kernel<N, HALVES><<<n_ctas, C::THREADS, C::SMEM, s>>>(map, a);
+  qgemm_q4k_tc_kernel<N><<<n_ctas, C::THREADS, C::SMEM, s>>>(map, a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
-// Kernel variant knobs (read once per process): SWARMLLM_QGEMM_HALVES=0|1,
-// SWARMLLM_QGEMM_POLL_NS=<ns back-off between failed barrier polls>.
-static int q_env(const char* name, int dflt) {
-  const char* v = getenv(name);
-  return v ? atoi(v) : dflt;
-}
-static const int g_q_halves = q_env("SWARMLLM_QGEMM_HALVES", 0);
-static const int g_q_poll = q_env("SWARMLLM_QGEMM_POLL_NS", 0);
-
-template <int N>
-static int launch_n(const CUtensorMap& map, const QGemmArgs& a, int n_ctas, cudaStream_t s) {
-  return g_q_halves ? launch_nh<N, true>(map, a, n_ctas, s) : launch_nh<N, false>(map, a, n_ctas, s);
-}
 
 int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, int x_stride,
                         int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
@@ -533,30 +457,6 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
   size_t need;
   q4k_tc_plan(rows, K, T, num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need);
   if (need > ws_floats_avail) return -6;
-  CUtensorMap map;
-  if (make_tmap_2d_16bit(&map, x, T, K, x_stride, N, 64, 128) != 0) return -2;
-  QGemmArgs a{(const uint8_t*)w_packed, rows, K, T, ntt, kb, total, upc, ws, status, g_trace};
-  a.n_peers = 0;
-  a.sig_ctl = nullptr;
-  a.poll_ns = (uint32_t)g_q_poll;
-  if (n_peers > 0) {
-    if (n_peers > 8 || !peer_ws || !sig_ctl || !sig_bases) return -7;
-    a.n_peers = n_peers;
-    for (int i = 0; i < n_peers; ++i) {
-      a.peer_ws[i] = peer_ws[i];
-      a.sig_bases[i] = sig_bases[i];
-    }
-    a.sig_ctl = sig_ctl;
-    a.sig_flag_off = sig_flag_off;
-    a.sig_rank = sig_rank;
-  }
-  int rc;
-  switch (N) {
-    case 16: rc = launch_n<16>(map, a, ctas, s); break;
-    case 32: rc = launch_n<32>(map, a, ctas, s); break;
-    case 64: rc = launch_n<64>(map, a, ctas, s); break;
-    default: rc = launch_n<128>(map, a, ctas, s); break;
-  }
   if (out) {
     out->ws = ws;
     out->rows = rows;
@@ -568,7 +468,31 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
     out->n_tok_tiles = ntt;
     out->seg_max = 0;
   }
-  return rc;
+  if (T <= g_gemv_max_t)
+    return launch_qgemv_q4k(w_packed, rows, K, x, x_stride, T, ws, kb, total, upc, ctas, status,
+                            peer_ws, n_peers, sig_ctl, sig_bases, sig_flag_off, sig_rank, s);
+  CUtensorMap map;
+  if (make_tmap_2d_16bit(&map, x, T, K, x_stride, N, 64, 128) != 0) return -2;
+  QGemmArgs a{(const uint8_t*)w_packed, rows, K, T, ntt, kb, total, upc, ws, status, g_trace};
+  a.n_peers = 0;
+  a.sig_ctl = nullptr;
+  if (n_peers > 0) {
+    if (n_peers > 8 || !peer_ws || !sig_ctl || !sig_bases) return -7;
+    a.n_peers = n_peers;
+    for (int i = 0; i < n_peers; ++i) {
+      a.peer_ws[i] = peer_ws[i];
+      a.sig_bases[i] = sig_bases[i];
+    }
+    a.sig_ctl = sig_ctl;
+    a.sig_flag_off = sig_flag_off;
+    a.sig_rank = sig_rank;
+  }
+  switch (N) {
+    case 16: return launch_n<16>(map, a, ctas, s);
+    case 32: return launch_n<32>(map, a, ctas, s);
+    case 64: return launch_n<64>(map, a, ctas, s);
+    default: return launch_n<128>(map, a, ctas, s);
+  }
 }
 
 int launch_q4k_repack(const void* src, int rows, int K, void* dst, cudaStream_t s) {

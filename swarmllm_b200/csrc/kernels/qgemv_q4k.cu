@@ -1,0 +1,327 @@
+// Q4_K x fp16 GEMV for decode at 1..2 tokens, on the CUDA cores.
+//
+//   out[t][r] = sum_k W[r][k] * X[t][k],   W: Q4_K (repacked, as qgemm_tc.cu), X: fp16 [T, K]
+//
+// At a handful of tokens the GEMM is a weight stream.  On the tensor cores a
+// 128 x N x 16 tcgen05.mma costs the same ~48 clocks for every N <= 64 and
+// the hand-offs around it stretch that further, so the swap-AB kernel tops
+// out near a third of HBM bandwidth there; this kernel instead spends about
+// 13 issue slots per 8 weights per warp lane and keeps HBM the limit.
+// (Reference: the mmvq dp4a path for <= 8 rows, candle quantized/cuda.rs:291;
+// activations stay fp16 here instead of being quantized to int8.)
+//
+// Layout and decomposition (shared with the tensor-core kernel, so the
+// stream-K partial format read by every epilogue -- gemm_out.cuh -- is the
+// same): a unit is (128-row tile, 256-K superblock); CTAs take contiguous
+// unit ranges; the partial of each tile segment goes to slot (tile + cta).
+// Inside a CTA, warp w owns rows [32w, 32w+32) of every unit: it streams its
+// 4.5 KB quarter of the unit (2 stages) and the unit's activations (T x 512 B,
+// 2 stages) into its own shared memory with bulk copies, so no warp ever
+// waits on another.  One lane = one weight row.
+//
+// Per 32-bit word of codes (8 weights, nibble order 0,2,4,6,1,3,5,7 from the
+// repack): LOP3 builds fp16 pairs 1024+q (low nibbles) or 1024+16q (high
+// nibbles); an HSUB2, resp. an HFMA2 by (1/16, -64), turns them into the exact
+// integers q; HFMA2 multiplies by the activation pair.  The sub-block scale
+// and min are applied once per 32 weights in fp32:
+//   sum_k (sc*q_k - m) x_k = sc * sum_k q_k x_k - m * sum_k x_k.
+// The fp16 partial sums hold 4 products each and are added in pairs (|sum| <=
+// 120 |x|max), so they stay finite for activations below ~500 in magnitude.
+#include "kernels.h"
+
+#include "common.cuh"
+#include "ep_common.cuh"
+#include "gemm_out.cuh"
+#include "qgemm_common.cuh"
+#include "tc_utils.cuh"
+
+namespace swarm {
+using namespace tc;
+
+constexpr int kGvWarps = 4;                          // one per 32-row quarter of a tile
+constexpr int kGvWStages = 2;                        // code stages per warp
+constexpr int kGvXStages = 2;                        // activation stages per warp
+constexpr int kGvQuarterBytes = 32 * kQ4kRowBytes;   // 4608
+// mbarriers of all warps, ahead of the stage buffers
+constexpr int kGvBarBytes = 256;
+static_assert(kGvWarps * (kGvWStages + kGvXStages) * 8 <= kGvBarBytes, "barrier area too small");
+
+template <int T>
+struct GvCfg {
+  static constexpr int X_STAGE = T * 512;                   // T x 256 fp16
+  static constexpr int WARP_BYTES = kGvWStages * kGvQuarterBytes + kGvXStages * X_STAGE;
+  static constexpr int SMEM = kGvBarBytes + kGvWarps * WARP_BYTES;
+  static_assert(WARP_BYTES % 16 == 0 && q4k_gemv_ctas_per_sm(T) * (SMEM + 1024) <= 228 * 1024,
+                "stage layout");
+};
+
+struct GemvArgs {
+  const uint8_t* w;
+  const __half* x;
+  int x_stride;   // elements
+  int rows, K;
+  int ksb;
+  long total_units;
+  int upc;
+  float* ws;
+  int* status;
+  int n_peers;
+  unsigned long long peer_ws[8];
+  int* sig_ctl;
+  unsigned long long sig_bases[8];
+  long long sig_flag_off;
+  int sig_rank;
+};
+
+SW_DEVICE __half2 u2h(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+
+template <int T>
+__global__ void __launch_bounds__(kGvWarps * 32)
+    qgemv_q4k_kernel(const __grid_constant__ GemvArgs a) {
+  using C = GvCfg<T>;
+  extern __shared__ __align__(128) uint8_t gv_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(gv_smem) + warp * (kGvWStages + kGvXStages);
+  uint64_t* xfull = wfull + kGvWStages;
+  uint8_t* wst = gv_smem + kGvBarBytes + warp * C::WARP_BYTES;
+  uint8_t* xst = wst + kGvWStages * kGvQuarterBytes;
+
+  const long u0 = (long)blockIdx.x * a.upc;
+  const long u1 = min(a.total_units, u0 + a.upc);
+  const int n = (int)max(0L, u1 - u0);
+
+  if (lane == 0) {
+    for (int s = 0; s < kGvWStages + kGvXStages; ++s) mbar_init(&wfull[s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  // bulk copies of unit i: this warp's 32 rows of codes, and the activations.
+  // A code stage is refilled as soon as its codes are in registers, an
+  // activation stage once the unit's dot products are done.  Units are walked
+  // with (tile, superblock) cursors: one division per CTA, none per unit.
+  const int rt0 = (int)(u0 / a.ksb), sb0 = (int)(u0 - (long)rt0 * a.ksb);
+  const uint8_t* wsrc = a.w + (((size_t)rt0 * a.ksb + sb0) * 128 + warp * 32) * kQ4kRowBytes;
+  int w_next = 0, x_next = 0, x_sb = sb0;   // lane 0's copy cursors
+  auto issue_w = [&]() {                    // codes of unit w_next (contiguous in the repack)
+    uint64_t* bar = &wfull[w_next % kGvWStages];
+    mbar_arrive_expect_tx(bar, kGvQuarterBytes);
+    bulk_load(wst + (w_next % kGvWStages) * kGvQuarterBytes,
+              wsrc + (size_t)w_next * (128 * kQ4kRowBytes), kGvQuarterBytes, bar);
+    ++w_next;
+  };
+  auto issue_x = [&]() {
+    uint64_t* bar = &xfull[x_next % kGvXStages];
+    mbar_arrive_expect_tx(bar, C::X_STAGE);
+#pragma unroll
+    for (int t = 0; t < T; ++t)
+      bulk_load(xst + (x_next % kGvXStages) * C::X_STAGE + t * 512,
+                a.x + (size_t)t * a.x_stride + (size_t)x_sb * 256, 512, bar);
+    ++x_next;
+    if (++x_sb == a.ksb) x_sb = 0;
+  };
+  if (lane == 0) {
+    while (w_next < min(n, kGvWStages)) issue_w();
+    while (x_next < min(n, kGvXStages)) issue_x();
+  }
+
+  const uint32_t MAGIC = 0x64006400u;
+  const __half2 K1024 = u2h(0x64006400u);
+  const __half2 SIXTEENTH = u2h(0x2C002C00u);   // 1/16, 1/16
+  const __half2 M64 = u2h(0xD400D400u);         // -64, -64
+  float acc[T];
+#pragma unroll
+  for (int t = 0; t < T; ++t) acc[t] = 0.f;
+
+  bool ok = true;
+  int rt = rt0, sb = sb0;
+  for (int i = 0; i < n; ++i) {
+    uint64_t* wb = &wfull[i % kGvWStages];
+    if (!(ok = mbar_wait_warp(wb, (i / kGvWStages) & 1, a.status, 41, i, warp))) break;
+    mbar_try_wait(smem_u32(wb), (i / kGvWStages) & 1);   // every lane acquires the bytes
+    const uint4* src = reinterpret_cast<const uint4*>(wst + (i % kGvWStages) * kGvQuarterBytes +
+                                                       lane * kQ4kRowBytes);
+    uint4 q[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) q[c] = src[c];
+    const uint4 hdr = src[8];
+    __syncwarp();
+    if (lane == 0 && w_next < n) issue_w();
+    float sc[8], mb[8];
+    q4k_decode_scales(hdr, sc, mb);
+    uint64_t* xb = &xfull[i % kGvXStages];
+    if (!(ok = mbar_wait_warp(xb, (i / kGvXStages) & 1, a.status, 42, i, warp))) break;
+    mbar_try_wait(smem_u32(xb), (i / kGvXStages) & 1);
+    const uint4* xs = reinterpret_cast<const uint4*>(xst + (i % kGvXStages) * C::X_STAGE);
+
+    // sum_j m_j * (sum of x over sub-block j): lane l sums x[8l, 8l+8); four
+    // lanes make a sub-block; every lane then needs all eight sub-block sums.
+    float msum[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      const uint4 v = xs[t * 32 + lane];
+      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(u2h(vw[e]));
+        s += f.x + f.y;
+      }
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      float m = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) m = fmaf(mb[j], __shfl_sync(0xffffffffu, s, 4 * j), m);
+      msum[t] = m;
+    }
+
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      // four independent fp16 sums (one per nibble pair) keep the chains short
+      __half2 p0[T], p1[T], p2[T], p3[T];
+#pragma unroll
+      for (int t = 0; t < T; ++t) p0[t] = p1[t] = p2[t] = p3[t] = __float2half2_rn(0.f);
+#pragma unroll
+      for (int w4 = 0; w4 < 4; ++w4) {
+        const uint32_t xw = qw[4 * j + w4], hi = xw >> 8;
+        // (k0,k1), (k2,k3), (k4,k5), (k6,k7) as exact fp16 integers
+        const __half2 c0 = __hsub2(u2h((xw & 0x000F000Fu) | MAGIC), K1024);
+        const __half2 c1 = __hfma2(u2h((xw & 0x00F000F0u) | MAGIC), SIXTEENTH, M64);
+        const __half2 c2 = __hsub2(u2h((hi & 0x000F000Fu) | MAGIC), K1024);
+        const __half2 c3 = __hfma2(u2h((hi & 0x00F000F0u) | MAGIC), SIXTEENTH, M64);
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const uint4 xv = xs[t * 32 + 4 * j + w4];   // x[8w .. 8w+8) of this word
+          p0[t] = __hfma2(c0, u2h(xv.x), p0[t]);
+          p1[t] = __hfma2(c1, u2h(xv.y), p1[t]);
+          p2[t] = __hfma2(c2, u2h(xv.z), p2[t]);
+          p3[t] = __hfma2(c3, u2h(xv.w), p3[t]);
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        const float2 f0 = __half22float2(__hadd2(p0[t], p1[t]));
+        const float2 f1 = __half22float2(__hadd2(p2[t], p3[t]));
+        acc[t] = fmaf(sc[j], (f0.x + f0.y) + (f1.x + f1.y), acc[t]);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) acc[t] -= msum[t];
+
+    __syncwarp();   // every lane is done with this activation stage
+    if (lane == 0 && x_next < n) issue_x();
+    if (i == n - 1 || sb == a.ksb - 1) {
+      // tile segment done: partial into slot (tile + cta), token rows 0..T-1 of 16
+      const size_t off = ((size_t)(rt + blockIdx.x) * 16) * 128 + warp * 32 + lane;
+      if (a.n_peers == 0) {
+#pragma unroll
+        for (int t = 0; t < T; ++t) a.ws[off + (size_t)t * 128] = acc[t];
+      } else {
+        for (int o = 0; o < a.n_peers; ++o) {
+          float* dst = reinterpret_cast<float*>(a.peer_ws[o]) + off;
+#pragma unroll
+          for (int t = 0; t < T; ++t) dst[(size_t)t * 128] = acc[t];
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < T; ++t) acc[t] = 0.f;
+    }
+    if (++sb == a.ksb) {
+      sb = 0;
+      ++rt;
+    }
+  }
+  if (!ok && lane == 0) {  // let this warp's copies still in flight land before exiting
+    for (int i = max(0, w_next - kGvWStages); i < w_next; ++i)
+      mbar_wait(&wfull[i % kGvWStages], (i / kGvWStages) & 1, nullptr, 0);
+    for (int i = max(0, x_next - kGvXStages); i < x_next; ++i)
+      mbar_wait(&xfull[i % kGvXStages], (i / kGvXStages) & 1, nullptr, 0);
+  }
+  __syncwarp();
+  if (a.sig_ctl != nullptr)   // all threads of every CTA (it syncs the CTA itself)
+    ep_grid_done_signal(a.sig_ctl, a.sig_bases, a.sig_flag_off, a.n_peers, a.sig_rank);
+}
+
+// The plan assumes q4k_gemv_ctas_per_sm(T) CTAs resident per SM (one wave);
+// ask for the full shared-memory carveout so they fit.
+template <int T>
+static int setup_t() {
+  static int state = 0;   // 0 unset, 1 ok, <0 error
+  if (state == 0) {
+    state = (cudaFuncSetAttribute(qgemv_q4k_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  GvCfg<T>::SMEM) == cudaSuccess &&
+             cudaFuncSetAttribute(qgemv_q4k_kernel<T>,
+                                  cudaFuncAttributePreferredSharedMemoryCarveout, 100) == cudaSuccess)
+                ? 1 : -3;
+  }
+  return state;
+}
+
+template <int T>
+static int occupancy_t() {
+  if (setup_t<T>() != 1) return -1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qgemv_q4k_kernel<T>, kGvWarps * 32,
+                                                    GvCfg<T>::SMEM) != cudaSuccess)
+    return -1;
+  return n;
+}
+
+template <int T>
+static int launch_t(const GemvArgs& a, int ctas, cudaStream_t s) {
+  if (setup_t<T>() != 1) return -3;
+  qgemv_q4k_kernel<T><<<ctas, kGvWarps * 32, GvCfg<T>::SMEM, s>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+}  // namespace swarm
+
+using namespace swarm;
+
+int q4k_gemv_occupancy(int T) {
+  switch (T) {
+    case 1: return occupancy_t<1>();
+    case 2: return occupancy_t<2>();
+    default: return 0;
+  }
+}
+
+int launch_qgemv_q4k(const void* w_packed, int rows, int K, const __half* x, int x_stride, int T,
+                     float* ws, int ksb, long total_units, int upc, int ctas, int* status,
+                     const unsigned long long* peer_ws, int n_peers, int* sig_ctl,
+                     const unsigned long long* sig_bases, long long sig_flag_off, int sig_rank,
+                     cudaStream_t s) {
+  if (T < 1 || T > kQGemvMaxT) return -1;
+  if ((x_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(w_packed) & 15) != 0)
+    return -5;
+  GemvArgs a{};
+  a.w = static_cast<const uint8_t*>(w_packed);
+  a.x = x;
+  a.x_stride = x_stride;
+  a.rows = rows;
+  a.K = K;
+  a.ksb = ksb;
+  a.total_units = total_units;
+  a.upc = upc;
+  a.ws = ws;
+  a.status = status;
+  a.n_peers = 0;
+  a.sig_ctl = nullptr;
+  if (n_peers > 0) {
+    if (n_peers > 8 || !peer_ws || !sig_ctl || !sig_bases) return -7;
+    a.n_peers = n_peers;
+    for (int i = 0; i < n_peers; ++i) {
+      a.peer_ws[i] = peer_ws[i];
+      a.sig_bases[i] = sig_bases[i];
+    }
+    a.sig_ctl = sig_ctl;
+    a.sig_flag_off = sig_flag_off;
+    a.sig_rank = sig_rank;
+  }
+  switch (T) {
+    case 1: return launch_t<1>(a, ctas, s);
+    default: return launch_t<2>(a, ctas, s);
+  }
+}

@@ -30,7 +30,7 @@ def stream_k_floats(max_tokens: int, rows: int, num_sms: int) -> int:
             continue
         n_tok = C().q4k_tc_plan(128, 256, T, num_sms)[0]
         tiles = (rows + 127) // 128 * ((T + n_tok - 1) // n_tok)
-        need = max(need, (tiles + num_sms) * n_tok * 128)
+        need = max(need, (tiles + C().q4k_plan_max_ctas(T, num_sms)) * n_tok * 128)
     return need
 
 

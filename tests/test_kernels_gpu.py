@@ -70,6 +70,28 @@ def test_qgemm_q4k_tc(rows, K, T):
     assert e < 3e-3, e
 
 
+@pytest.mark.parametrize("rows,K", [(384, 1024), (1280, 8192)])
+@pytest.mark.parametrize("T", [1, 2])
+def test_qgemv_q4k_strided(rows, K, T):
+    """Decode sizes run the CUDA-core GEMV; activations as a strided view."""
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    from swarmllm_b200.utils.ext import C
+    assert T <= C().q4k_gemv_max_t()
+    rng = np.random.default_rng(rows + 7 * T)
+    w = rng.standard_normal((rows, K), dtype=np.float32) * 0.02
+    b = Q.quantize(w, Q.Q4_K)
+    wd = torch.from_numpy(Q.dequantize(b, Q.Q4_K))
+    big = _x(T, K + 64, seed=3 * T) * 4.0
+    x = big[:, 8:K + 8]                       # row stride K + 64, 16-byte aligned start
+    ref = x.float() @ wd.T
+    ws = GemmWorkspace(DEV, 3, rows)
+    lin = QLinear(b, Q.Q4_K, rows, K, DEV)
+    out = _dense_from(lin(big.to(DEV)[:, 8:K + 8], ws), T, rows)
+    torch.cuda.synchronize()
+    ws.check()
+    assert rel_err(out.cpu(), ref) < 3e-3
+
+
 def test_q4k_repack_matches_host():
     rows, K = 256, 512
     rng = np.random.default_rng(3)
