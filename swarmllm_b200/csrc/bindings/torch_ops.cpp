@@ -39,6 +39,8 @@ void epi_rope_kv(const GemmResult& g, OptT bias, Tensor positions, OptT slots, T
   CHECK_DT(positions, at::kInt); CHECK_DT(q_out, at::kHalf); CHECK_DT(inv_freq, at::kFloat);
   TORCH_CHECK(g.g.rows == (n_q * (gate_out.has_value() ? 2 : 1) + 2 * n_kv) * head_dim,
               "QKV rows mismatch");
+  TORCH_CHECK(head_dim % 4 == 0 && rope_dim % 2 == 0 && rope_dim <= head_dim,
+              "head_dim must be a multiple of 4 and rope_dim even");
   const at::cuda::CUDAGuard guard(q_out.device());
   launch_epi_rope_kv(g.g, ptr_or_null<float>(bias), positions.data_ptr<int32_t>(),
                      ptr_or_null<int32_t>(slots), inv_freq.data_ptr<float>(), (int)n_q, (int)n_kv,

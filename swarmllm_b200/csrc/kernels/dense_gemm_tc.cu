@@ -228,6 +228,7 @@ int launch_dense_gemm_tc(const __half* w, int rows, int K, int w_stride, const _
   size_t need;
   dense_tc_plan(rows, K, T, num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need);
   if (need > ws_floats_avail) return -6;
+  if (total >= (1L << 24)) return -8;   // GemmOut's segment lookup assumes fewer units
   CUtensorMap wm, xm;
   if (make_tmap_2d_16bit(&wm, w, rows, K, w_stride, 128, 64, 128) != 0) return -2;
   if (make_tmap_2d_16bit(&xm, x, T, K, x_stride, N, 64, 128) != 0) return -2;
@@ -249,6 +250,7 @@ int launch_dense_gemm_tc(const __half* w, int rows, int K, int w_stride, const _
     out->tok_tile = N;
     out->n_tok_tiles = ntt;
     out->seg_max = 0;
+    gemm_out_finalize(out);
   }
   return rc;
 }

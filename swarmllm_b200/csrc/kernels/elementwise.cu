@@ -66,11 +66,26 @@ __global__ void epi_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ resid
   const int dim = g.rows;
   float* rr = residual + (size_t)t * dim;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < dim; i += kThreads) {
-    float v = rr[i] + g.get(t, i) + (bias ? bias[i] : 0.f);
-    rr[i] = v;
-    row[i] = v;
-    ss += v * v;
+  if ((dim & 3) == 0 && (reinterpret_cast<uintptr_t>(residual) & 15) == 0) {
+    // four rows per thread and step: 16-byte loads, more bytes in flight
+    for (int i = 4 * threadIdx.x; i < dim; i += 4 * kThreads) {
+      const float4 gv = g.get4(t, i);
+      float4 v = *reinterpret_cast<const float4*>(rr + i);
+      v.x += gv.x + (bias ? bias[i] : 0.f);
+      v.y += gv.y + (bias ? bias[i + 1] : 0.f);
+      v.z += gv.z + (bias ? bias[i + 2] : 0.f);
+      v.w += gv.w + (bias ? bias[i + 3] : 0.f);
+      *reinterpret_cast<float4*>(rr + i) = v;
+      *reinterpret_cast<float4*>(row + i) = v;
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+  } else {
+    for (int i = threadIdx.x; i < dim; i += kThreads) {
+      float v = rr[i] + g.get(t, i) + (bias ? bias[i] : 0.f);
+      rr[i] = v;
+      row[i] = v;
+      ss += v * v;
+    }
   }
   if (out == nullptr) return;
   ss = block_sum(ss, red);
@@ -105,21 +120,37 @@ __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
   const int page = slot >= 0 ? slot / page_size : 0, off = slot >= 0 ? slot - page * page_size : 0;
   const int q_rows = n_q * head_dim;
   const bool gated = gate_out != nullptr;
-  // Stage this CTA's q/k heads (pre-RoPE) in shared memory; v goes straight to the cache.
-  for (int i = threadIdx.x; i < nh * head_dim; i += blockDim.x) {
-    const int hh = h0 + i / head_dim, d = i - (i / head_dim) * head_dim;
+  // Stage this CTA's q/k heads (pre-RoPE) in shared memory; v goes straight to
+  // the cache.  Four consecutive dims per step (16-byte partial reads); head_dim
+  // and the row offsets are multiples of 4.
+  for (int i = 4 * threadIdx.x; i < nh * head_dim; i += 4 * blockDim.x) {
+    const int j = i / head_dim, d = i - j * head_dim;
+    const int hh = h0 + j;
     const int lr = hh * head_dim + d;  // logical row
     const int gr = gated ? (hh < n_q ? lr + hh * head_dim : lr + q_rows) : lr;
-    const float v = g.get(t, gr) + (bias ? bias[lr] : 0.f);
+    float4 v = g.get4(t, gr);
+    if (bias) {
+      v.x += bias[lr];
+      v.y += bias[lr + 1];
+      v.z += bias[lr + 2];
+      v.w += bias[lr + 3];
+    }
     if (hh < n_q + n_kv) {
-      sh[i] = v;
+      *reinterpret_cast<float4*>(sh + i) = v;
       if (gated && hh < n_q) {
-        const float gv = g.get(t, gr + head_dim);
-        gate_out[(size_t)t * q_rows + lr] = __float2half_rn(1.f / (1.f + __expf(-gv)));
+        const float4 gv = g.get4(t, gr + head_dim);
+        __half* go = gate_out + (size_t)t * q_rows + lr;
+        go[0] = __float2half_rn(1.f / (1.f + __expf(-gv.x)));
+        go[1] = __float2half_rn(1.f / (1.f + __expf(-gv.y)));
+        go[2] = __float2half_rn(1.f / (1.f + __expf(-gv.z)));
+        go[3] = __float2half_rn(1.f / (1.f + __expf(-gv.w)));
       }
     } else if (slot >= 0) {
       const int hv = hh - n_q - n_kv;
-      v_cache[(((size_t)page * n_kv + hv) * page_size + off) * head_dim + d] = __float2half_rn(v);
+      __align__(8) __half h4[4] = {__float2half_rn(v.x), __float2half_rn(v.y),
+                                   __float2half_rn(v.z), __float2half_rn(v.w)};
+      *reinterpret_cast<uint2*>(v_cache + (((size_t)page * n_kv + hv) * page_size + off) * head_dim +
+                                d) = *reinterpret_cast<const uint2*>(h4);
     }
   }
   __syncthreads();
@@ -139,40 +170,47 @@ __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
     }
     __syncthreads();
   }
-  const int half = rope_dim / 2;
-  // Rotate pairs; unrotated tail dims are copied.
-  for (int i = threadIdx.x; i < nh * head_dim; i += blockDim.x) {
-    const int j = i / head_dim, d = i - j * head_dim;
+  const int half = rope_dim / 2, hd2 = head_dim / 2;
+  // One thread per dimension pair: rotated pairs share one sincos; the
+  // unrotated tail (partial RoPE) is copied pairwise.
+  for (int i = threadIdx.x; i < nh * hd2; i += blockDim.x) {
+    const int j = i / hd2, p = i - j * hd2;
     const int hh = h0 + j;
     if (hh >= n_q + n_kv) continue;
     const float* x = sh + j * head_dim;
-    float y;
-    if (d < rope_dim) {
-      int fi, partner;
-      bool first;
+    int d0, d1;
+    float y0, y1;
+    if (p < half) {
       if (neox) {
-        fi = (d < half) ? d : d - half;
-        first = d < half;
-        partner = first ? d + half : d - half;
+        d0 = p;
+        d1 = p + half;
       } else {
-        fi = d >> 1;
-        first = (d & 1) == 0;
-        partner = first ? d + 1 : d - 1;
+        d0 = 2 * p;
+        d1 = 2 * p + 1;
       }
       float sn, cs;
-      sincosf((float)pos * inv_freq[fi], &sn, &cs);
+      sincosf((float)pos * inv_freq[p], &sn, &cs);
       cs *= attn_factor;
       sn *= attn_factor;
-      y = first ? (x[d] * cs - x[partner] * sn) : (x[partner] * sn + x[d] * cs);
+      y0 = x[d0] * cs - x[d1] * sn;
+      y1 = x[d1] * cs + x[d0] * sn;
     } else {
-      y = x[d];
+      d0 = rope_dim + 2 * (p - half);
+      d1 = d0 + 1;
+      y0 = x[d0];
+      y1 = x[d1];
     }
+    __half* dst;
     if (hh < n_q) {
-      q_out[((size_t)t * n_q + hh) * head_dim + d] = __float2half_rn(y);
+      dst = q_out + ((size_t)t * n_q + hh) * head_dim;
     } else if (slot >= 0) {
       const int hk = hh - n_q;
-      k_cache[(((size_t)page * n_kv + hk) * page_size + off) * head_dim + d] = __float2half_rn(y);
+      dst = k_cache + (((size_t)page * n_kv + hk) * page_size + off) * head_dim;
+    } else {
+      continue;
     }
+    dst[d0] = __float2half_rn(y0);
+    dst[d1] = __float2half_rn(y1);
   }
 }
 
@@ -183,6 +221,28 @@ __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int
                                   int interleaved, float alpha, float limit,
                                   __half* __restrict__ out) {
   const int t = blockIdx.y;
+  if (!interleaved && (F & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0) {
+    // four features per thread and step, 16-byte loads
+    for (int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x); i < F; i += 4 * gridDim.x * blockDim.x) {
+      const float4 g4 = g.get4(t, i), u4 = g.get4(t, F + i);
+      const float gs[4] = {g4.x, g4.y, g4.z, g4.w}, us[4] = {u4.x, u4.y, u4.z, u4.w};
+      __align__(8) __half y[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float gv = gs[e] + (bias ? bias[i + e] : 0.f);
+        float uv = us[e] + (bias ? bias[F + i + e] : 0.f);
+        if (kind == 0) {
+          y[e] = __float2half_rn(silu(gv) * uv);
+        } else {
+          gv = fminf(gv, limit);
+          uv = fminf(fmaxf(uv, -limit), limit);
+          y[e] = __float2half_rn(gv / (1.f + __expf(-alpha * gv)) * (uv + 1.f));
+        }
+      }
+      *reinterpret_cast<uint2*>(out + (size_t)t * F + i) = *reinterpret_cast<const uint2*>(y);
+    }
+    return;
+  }
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < F; i += gridDim.x * blockDim.x) {
     const int rg = interleaved ? 2 * i : i;
     const int ru = interleaved ? 2 * i + 1 : F + i;
@@ -203,6 +263,20 @@ __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int
 __global__ void epi_copy_kernel(GemmOut g, const float* __restrict__ bias, float* __restrict__ out,
                                 int out_stride) {
   const int t = blockIdx.y;
+  if ((g.rows & 3) == 0 && (out_stride & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+    for (int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x); i < g.rows;
+         i += 4 * gridDim.x * blockDim.x) {
+      float4 v = g.get4(t, i);
+      if (bias) {
+        v.x += bias[i];
+        v.y += bias[i + 1];
+        v.z += bias[i + 2];
+        v.w += bias[i + 3];
+      }
+      *reinterpret_cast<float4*>(out + (size_t)t * out_stride + i) = v;
+    }
+    return;
+  }
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < g.rows; i += gridDim.x * blockDim.x)
     out[(size_t)t * out_stride + i] = g.get(t, i) + (bias ? bias[i] : 0.f);
 }

@@ -35,17 +35,29 @@ struct GemmOut {
   long long src_stride;
   const float* add;  // optional dense [T][add_stride] term added on read (LoRA deltas)
   int add_stride;
+  // set by gemm_out_finalize(): every element read divides by neither
+  int tok_shift;     // log2(tok_tile)
+  float inv_upc;     // 1 / upc
 
 #ifdef __CUDACC__
+  // floor(u / upc) from a float estimate, corrected to the exact quotient
+  // (u < 2^24 keeps the estimate within one).
+  __device__ __forceinline__ int cta_of(int u) const {
+    int c = __float2int_rz((float)u * inv_upc);
+    if (c * upc > u) --c;
+    else if ((c + 1) * upc <= u) ++c;
+    return c;
+  }
+
   __device__ __forceinline__ float get(int t, int r) const {
     const float extra = add ? add[(size_t)t * add_stride + r] : 0.f;
     if (mode == 0) return ws[(size_t)t * rows + r] + extra;
     const int rt = r >> 7, rr = r & 127;
-    const int nt = t / tok_tile, tt = t - nt * tok_tile;
+    const int nt = t >> tok_shift, tt = t & (tok_tile - 1);
     const int tile = rt * n_tok_tiles + nt;
-    const long u0 = (long)tile * ksb;
-    const int c0 = (int)(u0 / upc);
-    const int c1 = (int)((u0 + ksb - 1) / upc);
+    const int u0 = tile * ksb;
+    const int c0 = cta_of(u0);
+    const int c1 = cta_of(u0 + ksb - 1);
     float acc = extra;
     const int ns = n_src > 1 ? n_src : 1;
     for (int s = 0; s < ns; ++s) {
@@ -54,7 +66,50 @@ struct GemmOut {
     }
     return acc;
   }
+
+  // Rows r..r+3 (r % 4 == 0) with 16-byte loads: four rows of one 128-row
+  // group are contiguous in every slot.  Needs rows % 4 == 0 (mode 0) and
+  // 16-byte aligned partial buffers (workspaces are).
+  __device__ __forceinline__ float4 get4(int t, int r) const {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (add) {
+      const float* a = add + (size_t)t * add_stride + r;
+      acc = make_float4(a[0], a[1], a[2], a[3]);
+    }
+    if (mode == 0) {
+      const float4 v = *reinterpret_cast<const float4*>(ws + (size_t)t * rows + r);
+      return make_float4(acc.x + v.x, acc.y + v.y, acc.z + v.z, acc.w + v.w);
+    }
+    const int rt = r >> 7, rr = r & 127;
+    const int nt = t >> tok_shift, tt = t & (tok_tile - 1);
+    const int tile = rt * n_tok_tiles + nt;
+    const int u0 = tile * ksb;
+    const int c0 = cta_of(u0);
+    const int c1 = cta_of(u0 + ksb - 1);
+    const int ns = n_src > 1 ? n_src : 1;
+    for (int s = 0; s < ns; ++s) {
+      const float* w = ws + (size_t)s * src_stride;
+      for (int c = c0; c <= c1; ++c) {
+        const float4 v =
+            *reinterpret_cast<const float4*>(w + ((size_t)(tile + c) * tok_tile + tt) * 128 + rr);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+    }
+    return acc;
+  }
 #endif
 };
+
+// Fill the derived fields of a stream-K GemmOut (host side, after tok_tile /
+// upc are set).  tok_tile is a power of two; unit counts stay below 2^24.
+inline void gemm_out_finalize(GemmOut* g) {
+  int s = 0;
+  while ((1 << s) < g->tok_tile) ++s;
+  g->tok_shift = s;
+  g->inv_upc = g->upc > 0 ? 1.0f / (float)g->upc : 0.f;
+}
 
 }  // namespace swarm

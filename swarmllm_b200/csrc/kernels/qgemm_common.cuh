@@ -20,14 +20,21 @@ constexpr int kQ4kRowBytes = 144;  // 128 B permuted nibbles + 16 B (d, dmin, sc
 
 // 8 permuted nibbles -> 4 fp16 pairs (K order), scale s, min mb.  The nibble
 // order (0,2,4,6,1,3,5,7) lets one mask produce (1024 + q) pairs.
+// (a & b) | c as one LOP3 (the compiler does not always fuse the pair)
+SW_DEVICE uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 SW_DEVICE void dq_word(uint32_t x, __half2 S, __half2 S16, __half2 MB, uint32_t* out) {
   const uint32_t MAGIC = 0x64006400u;
   const __half2 K1024 = u32_as_h2(0x64006400u);
   const uint32_t hi = x >> 8;
-  __half2 c0 = __hsub2(u32_as_h2((x & 0x000F000Fu) | MAGIC), K1024);
-  __half2 c1 = __hsub2(u32_as_h2((x & 0x00F000F0u) | MAGIC), K1024);
-  __half2 c2 = __hsub2(u32_as_h2((hi & 0x000F000Fu) | MAGIC), K1024);
-  __half2 c3 = __hsub2(u32_as_h2((hi & 0x00F000F0u) | MAGIC), K1024);
+  __half2 c0 = __hsub2(u32_as_h2(and_or(x, 0x000F000Fu, MAGIC)), K1024);
+  __half2 c1 = __hsub2(u32_as_h2(and_or(x, 0x00F000F0u, MAGIC)), K1024);
+  __half2 c2 = __hsub2(u32_as_h2(and_or(hi, 0x000F000Fu, MAGIC)), K1024);
+  __half2 c3 = __hsub2(u32_as_h2(and_or(hi, 0x00F000F0u, MAGIC)), K1024);
   out[0] = h2_as_u32(__hfma2(c0, S, MB));
   out[1] = h2_as_u32(__hfma2(c1, S16, MB));
   out[2] = h2_as_u32(__hfma2(c2, S, MB));

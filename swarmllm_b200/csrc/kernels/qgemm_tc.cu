@@ -457,6 +457,7 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
   size_t need;
   q4k_tc_plan(rows, K, T, num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need);
   if (need > ws_floats_avail) return -6;
+  if (total >= (1L << 24)) return -8;   // GemmOut's segment lookup assumes fewer units
   if (out) {
     out->ws = ws;
     out->rows = rows;
@@ -467,6 +468,7 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
     out->tok_tile = N;
     out->n_tok_tiles = ntt;
     out->seg_max = 0;
+    gemm_out_finalize(out);
   }
   if (T <= g_gemv_max_t)
     return launch_qgemv_q4k(w_packed, rows, K, x, x_stride, T, ws, kb, total, upc, ctas, status,

@@ -186,10 +186,10 @@ __global__ void __launch_bounds__(kGvWarps * 32)
       for (int w4 = 0; w4 < 4; ++w4) {
         const uint32_t xw = qw[4 * j + w4], hi = xw >> 8;
         // (k0,k1), (k2,k3), (k4,k5), (k6,k7) as exact fp16 integers
-        const __half2 c0 = __hsub2(u2h((xw & 0x000F000Fu) | MAGIC), K1024);
-        const __half2 c1 = __hfma2(u2h((xw & 0x00F000F0u) | MAGIC), SIXTEENTH, M64);
-        const __half2 c2 = __hsub2(u2h((hi & 0x000F000Fu) | MAGIC), K1024);
-        const __half2 c3 = __hfma2(u2h((hi & 0x00F000F0u) | MAGIC), SIXTEENTH, M64);
+        const __half2 c0 = __hsub2(u2h(and_or(xw, 0x000F000Fu, MAGIC)), K1024);
+        const __half2 c1 = __hfma2(u2h(and_or(xw, 0x00F000F0u, MAGIC)), SIXTEENTH, M64);
+        const __half2 c2 = __hsub2(u2h(and_or(hi, 0x000F000Fu, MAGIC)), K1024);
+        const __half2 c3 = __hfma2(u2h(and_or(hi, 0x00F000F0u, MAGIC)), SIXTEENTH, M64);
 #pragma unroll
         for (int t = 0; t < T; ++t) {
           const uint4 xv = xs[t * 32 + 4 * j + w4];   // x[8w .. 8w+8) of this word
