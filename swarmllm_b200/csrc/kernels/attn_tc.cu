@@ -12,6 +12,10 @@
 //   P  -> TMEM (fp16)   tcgen05.st
 //   O += P V            tcgen05.mma  A=P (TMEM)  B=V tile (smem, MN-major)
 //
+// For head_dim <= 128, S and P are double-buffered in TMEM and the MMA thread
+// issues QK^T of tile j+1 before P V of tile j, so the tensor core works while
+// the softmax of the previous tile runs.
+//
 // The fp32 O accumulator stays in TMEM; a row is rescaled in TMEM only when its
 // running max moves.  With one split the kernel finishes the softmax (adding
 // learned sinks) and writes fp16 output; with several it writes (O, max, sum)
@@ -38,7 +42,13 @@ struct AttnCfg {
   static constexpr int KV_TILE = kAttnKeys * D * 2;       // K or V tile
   static constexpr int ST = D <= 64 ? 4 : (D <= 128 ? 3 : 1);  // K/V tile stages
   static constexpr int SMEM = 1024 + Q_BYTES + ST * 2 * KV_TILE + 256;
-  static constexpr int S_COL = 0, P_COL = 128, O_COL = 256;
+  // DB: S and P double-buffered in TMEM, so QK^T of tile j+1 runs while the
+  // softmax of tile j does (needs D <= 128 for the columns).
+  static constexpr bool DB = D <= 128;
+  static constexpr int NB = DB ? 2 : 1;
+  __host__ __device__ static constexpr int s_col(int b) { return b * 128; }
+  __host__ __device__ static constexpr int p_col(int b) { return DB ? 256 + b * 64 : 128; }
+  static constexpr int O_COL = DB ? 384 : 256;
   static constexpr int THREADS = 192;                     // 4 softmax warps, producer, MMA
   static_assert(O_COL + D <= 512, "TMEM");
   static_assert(SMEM <= 227 * 1024, "smem");
@@ -76,7 +86,7 @@ SW_DEVICE float exp2_approx(float x) {
   return y;
 }
 
-template <int D, bool TREE>
+template <int D, bool TREE, int REP>
 __global__ void __launch_bounds__(192, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                    const __grid_constant__ CUtensorMap v_map, AttnTcArgs a) {
@@ -90,10 +100,12 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = q_full + 1;          // [ST]
   uint64_t* kv_empty = kv_full + C::ST;    // [ST]
-  uint64_t* s_full = kv_empty + C::ST;     // QK done
-  uint64_t* p_full = s_full + 1;           // P written (4 warps)
-  uint64_t* pv_done = p_full + 1;          // PV done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+  uint64_t* s_full = kv_empty + C::ST;     // [NB] QK done
+  uint64_t* p_full = s_full + C::NB;       // [NB] P written (4 warps)
+  uint64_t* pv_done = p_full + C::NB;      // PV done (one phase per tile)
+  uint64_t* o_done = pv_done + 1;          // every MMA of the CTA done (one phase)
+  uint64_t* rep_done = o_done + 1;         // replica partials staged (4 softmax warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rep_done + 1);
 
   const int g = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,9 +124,10 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < C::ST; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    for (int b = 0; b < C::NB; ++b) { mbar_init(&s_full[b], 1); mbar_init(&p_full[b], 4); }
     mbar_init(pv_done, 1);
+    mbar_init(o_done, 1);
+    mbar_init(rep_done, 4);
     fence_barrier_init();
   }
   if (warp == 5) {
@@ -132,10 +145,14 @@ __global__ void __launch_bounds__(192, 1)
       prefetch_tensormap(&q_map);
       prefetch_tensormap(&k_map);
       prefetch_tensormap(&v_map);
-      mbar_arrive_expect_tx(q_full, (uint32_t)(C::DH * a.n_rep * a.pos_per_group * 128));
+      // REP copies of the group's 8 rows, one per TMEM lane quadrant (rows
+      // 32k.., 4096-byte offsets, so the 128-byte swizzle of every copy matches)
+      mbar_arrive_expect_tx(q_full, (uint32_t)(REP * C::DH * a.n_rep * a.pos_per_group * 128));
 #pragma unroll
       for (int dh = 0; dh < C::DH; ++dh)
-        tma_load_3d(q_s + dh * 128 * 128, &q_map, dh * 64, hk * a.n_rep, row0, q_full);
+#pragma unroll
+        for (int k = 0; k < REP; ++k)
+          tma_load_3d(q_s + dh * 128 * 128 + k * 4096, &q_map, dh * 64, hk * a.n_rep, row0, q_full);
       // Page ids of the next tile are read before waiting for a free stage, all
       // eight at once (the TMA asm is a compiler memory barrier, so reading them
       // inside the issue loop would serialise eight L2 round trips per tile).
@@ -178,44 +195,71 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t idesc_pv = idesc_f16(128, D, 0, /*a_mn*/ 0, /*b_mn*/ 1);
       const uint64_t qd = smem_desc(smem_u32(q_s), 16, 1024, 2);
       bool ok = mbar_wait(q_full, 0, a.status, 42, 0, 0);
-      for (int j = 0; j < n_tiles && ok; ++j) {
+      // S(j) = Q K(j)^T into S buffer b  (K over the head dim)
+      auto issue_qk = [&](int j) -> bool {
         const int st = j % C::ST;
-        if (!(ok = mbar_wait(&kv_full[st], (j / C::ST) & 1, a.status, 43, j, 0))) break;
+        if (!mbar_wait(&kv_full[st], (j / C::ST) & 1, a.status, 43, j, 0)) return false;
         ATRACE(a, j, 1);
         tc_fence_after();
-        const uint32_t kb = smem_u32(kv_s + st * 2 * C::KV_TILE);
-        const uint64_t kd = smem_desc(kb, 16, 1024, 2);
-        // S = Q K^T  (K over head dim)
+        const uint64_t kd = smem_desc(smem_u32(kv_s + st * 2 * C::KV_TILE), 16, 1024, 2);
+        const int b = C::DB ? (j & 1) : 0;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t off = (uint64_t)((((kk >> 2) * (kAttnKeys * 128)) + (kk & 3) * 32) >> 4);
           const uint64_t qoff = (uint64_t)((((kk >> 2) * (128 * 128)) + (kk & 3) * 32) >> 4);
-          umma_f16_ss(tmem + C::S_COL, qd + qoff, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
+          umma_f16_ss(tmem + C::s_col(b), qd + qoff, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        umma_commit(s_full);
+        umma_commit(&s_full[b]);
         ATRACE(a, j, 2);
+        return true;
+      };
+      // With DB, QK(j+1) is issued before PV(j): its S buffer was last read by
+      // the softmax of tile j-1, which finished before PV(j-1) was issued.
+      if (C::DB && ok && n_tiles > 0) ok = issue_qk(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j % C::ST;
+        if (C::DB) {
+          if (j + 1 < n_tiles && !(ok = issue_qk(j + 1))) break;
+        } else {
+          if (!(ok = issue_qk(j))) break;
+        }
         // O += P V  (K over keys); V tile is MN-major: LBO = d-block stride, SBO = 8 keys
-        if (!(ok = mbar_wait(p_full, j & 1, a.status, 44, j, 0))) break;
+        const int b = C::DB ? (j & 1) : 0;
+        if (!(ok = mbar_wait(&p_full[b], C::DB ? ((j >> 1) & 1) : (j & 1), a.status, 44, j, 0))) break;
         ATRACE(a, j, 5);
         tc_fence_after();
+        const uint32_t kb = smem_u32(kv_s + st * 2 * C::KV_TILE);
         const uint64_t vd = smem_desc(kb + C::KV_TILE, kAttnKeys * 128, 1024, 2);
 #pragma unroll
         for (int kk = 0; kk < kAttnKeys / 16; ++kk)
-          umma_f16_ts(tmem + C::O_COL, tmem + C::P_COL + kk * 8,
+          umma_f16_ts(tmem + C::O_COL, tmem + C::p_col(b) + kk * 8,
                       vd + (uint64_t)((kk * 16 * 128) >> 4), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(pv_done);
         umma_commit(&kv_empty[st]);
       }
+      umma_commit(o_done);   // tracks everything this thread issued
     }
   } else {
     // ------------------------------------------------------------ softmax (thread = row)
-    const int r = threadIdx.x;  // 0..127
+    // REP == 4 (groups of exactly 8 rows, i.e. one decode position x 8 query
+    // heads): Q was loaded once per TMEM lane quadrant, so lanes 0..7 of every
+    // softmax warp hold the group's rows, and warp q owns keys [32q, 32q+32) of
+    // every tile (its P rows are zero elsewhere).  tcgen05.ld/st take one
+    // column address per warp, which is why a replica is a warp, not a lane.
+    // Each replica keeps its own running max and sum, so tiles need no
+    // cross-warp traffic; the four are merged like key-split partials at the
+    // end.  The softmax work of a tile is then spread over four schedulers
+    // and is a quarter as long.
+    constexpr int KW = kAttnKeys / REP;  // keys of a tile owned by one warp
+    const int m = threadIdx.x;           // TMEM lane / MMA row 0..127
+    const int rrow = REP == 1 ? m : lane;
+    const int kq = REP == 1 ? 0 : warp;
     const int quad = warp;      // warps 0..3 -> TMEM lane quadrants 0..3
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const bool real = r < nrows;
+    const bool real = REP == 1 ? (m < nrows) : (lane < 8);
     const bool warp_real = __any_sync(0xffffffffu, real);
-    const int pi = real ? r / a.n_rep : 0;
-    const int h = real ? r - pi * a.n_rep : 0;
+    const int pi = real ? rrow / a.n_rep : 0;
+    const int h = real ? rrow - pi * a.n_rep : 0;
     const int trow = row0 + pi;
     const int L = real ? a.seq_lens[trow] : 0;
     const int lo_win = (a.window > 0) ? max(0, L - a.window) : 0;
@@ -226,32 +270,46 @@ __global__ void __launch_bounds__(192, 1)
     // stays in fp16 range and O is rescaled in TMEM only a few times per row.
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    if (REP > 1) {  // P rows start zero: each replica writes only its keys
+      uint32_t z[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) z[e] = 0u;
+#pragma unroll
+      for (int b = 0; b < C::NB; ++b)
+#pragma unroll
+        for (int c = 0; c < kAttnKeys / 32; ++c) tmem_st_x16(tmem + lane_off + C::p_col(b) + c * 16, z);
+      tmem_wait_st();
+    }
     for (int j = 0; j < n_tiles && ok; ++j) {
-      // s_full(j) also covers PV(j-1): both were issued by the MMA thread and a
-      // commit tracks all of that thread's earlier tcgen05 operations.
-      if (!(ok = mbar_wait_warp(s_full, j & 1, a.status, 45, j, 0))) break;
+      // Without DB, s_full(j) also covers PV(j-1): a commit tracks all of the MMA
+      // thread's earlier tcgen05 operations.  With DB it covers PV(j-2), which
+      // is what reusing P buffer (j & 1) needs.
+      const int b = C::DB ? (j & 1) : 0;
+      if (!(ok = mbar_wait_warp(&s_full[b], C::DB ? ((j >> 1) & 1) : (j & 1), a.status, 45, j, 0)))
+        break;
       if (threadIdx.x == 0) ATRACE(a, j, 3);
       if (warp_real) {
         tc_fence_after();
-        const int key0 = k_lo + j * kAttnKeys;
-        float s[kAttnKeys];
+        const int key0 = k_lo + j * kAttnKeys + kq * KW;
+        float s[KW];
 #pragma unroll
-        for (int c = 0; c < kAttnKeys / 16; ++c)
-          tmem_ld_x16(tmem + lane_off + C::S_COL + c * 16, reinterpret_cast<uint32_t*>(s) + c * 16);
+        for (int c = 0; c < KW / 16; ++c)
+          tmem_ld_x16(tmem + lane_off + C::s_col(b) + kq * KW + c * 16,
+                      reinterpret_cast<uint32_t*>(s) + c * 16);
         tmem_wait_ld();
-        // visible keys of this row inside the tile: [vlo, vhi) (+ tree bits)
-        const int vlo = max(lo_win - key0, 0), vhi = min(L - key0, kAttnKeys);
+        // visible keys of this row inside its window: [vlo, vhi) (+ tree bits)
+        const int vlo = max(lo_win - key0, 0), vhi = min(L - key0, KW);
         float mt = -INFINITY;
-        const bool full = !TREE && __all_sync(0xffffffffu, vlo == 0 && vhi == kAttnKeys);
-        if (full) {  // whole tile visible for every row of the warp: no masking
+        const bool full = !TREE && __all_sync(0xffffffffu, vlo == 0 && vhi == KW);
+        if (full) {  // whole window visible for every row of the warp: no masking
 #pragma unroll
-          for (int c = 0; c < kAttnKeys; ++c) {
+          for (int c = 0; c < KW; ++c) {
             s[c] *= a.scale_log2;
             mt = fmaxf(mt, s[c]);
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < kAttnKeys; ++c) {
+          for (int c = 0; c < KW; ++c) {
             bool vis = c >= vlo && c < vhi;
             if (TREE) {
               const int k = key0 + c;
@@ -268,6 +326,12 @@ __global__ void __launch_bounds__(192, 1)
           m_new = mt;
         }
         if (__any_sync(0xffffffffu, m_new != m_run && m_run != -INFINITY)) {
+          // With DB, PV(j-1) may still be accumulating into O: wait for it.  (s_full(j)
+          // implies PV(j-2) is done, so pv_done is at most one phase behind here.)
+          if (C::DB && j > 0) {
+            if (!(ok = mbar_wait_warp(pv_done, (j - 1) & 1, a.status, 46, j, 0))) break;
+            tc_fence_after();
+          }
           const float alpha = (m_new != m_run && m_run != -INFINITY) ? exp2_approx(m_run - m_new) : 1.f;
           l_run *= alpha;
 #pragma unroll 1
@@ -282,13 +346,13 @@ __global__ void __launch_bounds__(192, 1)
         }
         m_run = m_new;
         float ls = 0.f;
-        uint32_t pk[kAttnKeys / 2];
+        uint32_t pk[KW / 2];
         // exp2(-inf - m) = 0, so masked keys need no special case (m_run is
         // finite whenever any key of the row is visible; otherwise all s are
         // -inf and m_run = -inf: clamp to keep p = 0 instead of NaN).
         const float msub = (m_run == -INFINITY) ? 0.f : m_run;
 #pragma unroll
-        for (int c = 0; c < kAttnKeys; c += 2) {
+        for (int c = 0; c < KW; c += 2) {
           const float p0 = exp2_approx(s[c] - msub);
           const float p1 = exp2_approx(s[c + 1] - msub);
           ls += p0 + p1;
@@ -297,17 +361,97 @@ __global__ void __launch_bounds__(192, 1)
         }
         l_run += ls;
 #pragma unroll
-        for (int c = 0; c < kAttnKeys / 32; ++c) tmem_st_x16(tmem + lane_off + C::P_COL + c * 16, pk + c * 16);
+        for (int c = 0; c < KW / 32; ++c)
+          tmem_st_x16(tmem + lane_off + C::p_col(b) + kq * (KW / 2) + c * 16, pk + c * 16);
         tmem_wait_st();
         tc_fence_before();
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[b]);
       if (threadIdx.x == 0) ATRACE(a, j, 4);
     }
     // ---- finish: wait for the last PV, then write output or partials
-    if (ok && n_tiles > 0) ok = mbar_wait_warp(pv_done, (n_tiles - 1) & 1, a.status, 47, 0, 0);
+    if (ok && n_tiles > 0)
+      ok = C::DB ? mbar_wait_warp(o_done, 0, a.status, 47, 0, 0)
+                 : mbar_wait_warp(pv_done, (n_tiles - 1) & 1, a.status, 47, 0, 0);
     if (ok) tc_fence_after();
+    if (REP > 1) {
+      // ---- merge the four replicas (warps) of each row through shared memory
+      // (the K/V stages are idle now: every tile was consumed before o_done)
+      float* red = reinterpret_cast<float*>(kv_s);          // [REP][8][2]  (max, sum)
+      float* obuf = red + REP * 8 * 2;                        // [REP][8][D]
+      if (real) {
+        red[(kq * 8 + lane) * 2 + 0] = m_run;
+        red[(kq * 8 + lane) * 2 + 1] = l_run;
+      }
+#pragma unroll 1
+      for (int c = 0; c < D / 16; ++c) {
+        uint32_t o[16];
+        if (n_tiles > 0) {
+          tmem_ld_x16(tmem + lane_off + C::O_COL + c * 16, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[e] = 0u;
+        }
+        if (real) {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) obuf[(kq * 8 + lane) * D + c * 16 + e] = __uint_as_float(o[e]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(rep_done);
+      const bool merged_ok = mbar_wait(rep_done, 0, a.status, 48, 0, 0);
+      // thread t: row t / 16, dims [(t % 16) * D / 16, +D / 16)
+      const int r = m >> 4, dd = (m & 15) * (D / 16);
+      float M = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < REP; ++k) M = fmaxf(M, red[(k * 8 + r) * 2]);
+      float f[REP], l = 0.f;
+#pragma unroll
+      for (int k = 0; k < REP; ++k) {
+        const float mk = red[(k * 8 + r) * 2];
+        f[k] = (mk == -INFINITY) ? 0.f : exp2_approx(mk - M);
+        l += f[k] * red[(k * 8 + r) * 2 + 1];
+      }
+      const int hq = hk * a.n_rep + r;
+      if (merged_ok && a.n_splits == 1) {
+        float oscale = 1.f;
+        if (a.sinks) {
+          const float sk = a.sinks[hq] * 1.4426950408889634f;
+          const float mm = fmaxf(M, sk);
+          const float fm = (M == -INFINITY) ? 0.f : exp2_approx(M - mm);
+          l = l * fm + exp2_approx(sk - mm);
+          oscale = fm;
+        }
+        const float inv = l > 0.f ? oscale / l : 0.f;
+        __half* dst = a.out + ((size_t)row0 * a.n_q + hq) * D + dd;
+#pragma unroll
+        for (int e = 0; e < D / 16; e += 2) {
+          float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+          for (int k = 0; k < REP; ++k) {
+            v0 += f[k] * obuf[(k * 8 + r) * D + dd + e];
+            v1 += f[k] * obuf[(k * 8 + r) * D + dd + e + 1];
+          }
+          *reinterpret_cast<__half2*>(dst + e) = __floats2half2_rn(v0 * inv, v1 * inv);
+        }
+      } else if (merged_ok) {
+        const size_t pb = ((size_t)row0 * a.n_q + hq) * a.n_splits + sp;
+        float* po = a.part_o + pb * D + dd;
+#pragma unroll
+        for (int e = 0; e < D / 16; ++e) {
+          float v = 0.f;
+#pragma unroll
+          for (int k = 0; k < REP; ++k) v += f[k] * obuf[(k * 8 + r) * D + dd + e];
+          po[e] = v;
+        }
+        if ((m & 15) == 0) {
+          a.part_ml[pb * 2 + 0] = (n_tiles > 0 && M != -INFINITY) ? M * 0.6931471805599453f : -INFINITY;
+          a.part_ml[pb * 2 + 1] = l;
+        }
+      }
+    } else {
     const int hq = hk * a.n_rep + h;
     if (warp_real && a.n_splits == 1) {
       float oscale = 1.f;
@@ -355,6 +499,7 @@ __global__ void __launch_bounds__(192, 1)
         a.part_ml[pb * 2 + 0] = (n_tiles > 0 && m_run != -INFINITY) ? m_run * 0.6931471805599453f : -INFINITY;
         a.part_ml[pb * 2 + 1] = l_run;
       }
+    }
     }
   }
   tc_fence_before();
@@ -424,18 +569,22 @@ static int launch_d(const CUtensorMap& qm, const CUtensorMap& km, const CUtensor
   using C = AttnCfg<D>;
   static bool attr = false;
   if (!attr) {
-    if (cudaFuncSetAttribute(attn_tc_kernel<D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(attn_tc_kernel<D, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_tc_kernel<D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(attn_tc_kernel<D, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_tc_kernel<D, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM) != cudaSuccess)
       return -3;
     attr = true;
   }
   dim3 grid(G, a.n_kv, a.n_splits);
   if (a.tree_mask != nullptr)
-    attn_tc_kernel<D, true><<<grid, C::THREADS, C::SMEM, s>>>(qm, km, vm, a);
+    attn_tc_kernel<D, true, 1><<<grid, C::THREADS, C::SMEM, s>>>(qm, km, vm, a);
+  else if (a.n_rep * a.pos_per_group == 8)  // 8-row groups (decode, 8 heads per KV head)
+    attn_tc_kernel<D, false, 4><<<grid, C::THREADS, C::SMEM, s>>>(qm, km, vm, a);
   else
-    attn_tc_kernel<D, false><<<grid, C::THREADS, C::SMEM, s>>>(qm, km, vm, a);
+    attn_tc_kernel<D, false, 1><<<grid, C::THREADS, C::SMEM, s>>>(qm, km, vm, a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

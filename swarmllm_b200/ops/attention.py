@@ -6,6 +6,8 @@ fp16, 16-token pages.  A (page, kv head) is one contiguous 4 KB run
 """
 from __future__ import annotations
 
+import functools
+
 import torch
 
 from ..utils.ext import C
@@ -58,15 +60,24 @@ class PagedKVCache:
         d[:, :, dp, :, do, :] = rows
 
 
+@functools.lru_cache(maxsize=4096)
 def tc_split_plan(n_groups: int, n_kv: int, max_len: int, num_sms: int = 148,
                   max_splits: int = 32) -> tuple[int, int]:
-    """(keys_per_split, n_splits) for the tcgen05 kernel: whole 128-key tiles,
-    enough CTAs for about two waves."""
+    """(keys_per_split, n_splits) for the tcgen05 kernel (one CTA per SM, whole
+    128-key tiles): the split count that minimises waves x (tiles per CTA + 1),
+    the +1 standing for a CTA's fixed start-up (TMEM, barriers, Q and first
+    K/V loads).  Fewer splits win ties (less combine work)."""
     tiles = max(1, (max_len + 127) // 128)
     ctas = max(1, n_groups * n_kv)
-    want = max(1, min(tiles, max_splits, (2 * num_sms + ctas - 1) // ctas))
-    tps = (tiles + want - 1) // want
-    return tps * 128, (tiles + tps - 1) // tps
+    best = None
+    for want in range(1, min(tiles, max_splits) + 1):
+        tps = (tiles + want - 1) // want
+        ns = (tiles + tps - 1) // tps
+        waves = (ctas * ns + num_sms - 1) // num_sms
+        cost = waves * (tps + 1)
+        if best is None or cost < best[0]:
+            best = (cost, tps, ns)
+    return best[1] * 128, best[2]
 
 
 class AttentionWorkspace:
@@ -79,12 +90,14 @@ class AttentionWorkspace:
         t = 1
         while True:
             tt = min(t, max_rows)
-            worst = max(worst, tt * split_plan(tt, n_kv, max_len, num_sms, max_splits)[1],
-                        tt * tc_split_plan(tt, n_kv, max_len, num_sms, max_splits)[1])
+            worst = max(worst, tt * split_plan(tt, n_kv, max_len, num_sms, max_splits)[1])
             if tt == max_rows:
                 break
             t *= 2
         worst *= 2  # T * n_splits(T) between powers of two is at most twice the sampled max
+        # the tensor-core plan is not monotone in T: take its exact maximum
+        worst = max(worst, max(tt * tc_split_plan(tt, n_kv, max_len, num_sms, max_splits)[1]
+                               for tt in range(1, max_rows + 1)))
         self.part_o = torch.empty(worst * n_q * head_dim, dtype=torch.float32, device=device)
         self.part_ml = torch.empty(worst * n_q * 2, dtype=torch.float32, device=device)
         self.n_q, self.head_dim = n_q, head_dim
