@@ -345,6 +345,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                             R, rows, u.data_ptr<float>(), delta.data_ptr<float>(), cur_stream()) == 0,
                 "lora launch failed");
   });
+  m.def("dequant_f16", [](Tensor raw, int64_t qtype, int64_t rows, int64_t K, Tensor out) {
+    CHECK_CUDA(raw); CHECK_DT(out, at::kHalf); CHECK_CONTIG(out);
+    TORCH_CHECK(out.numel() >= rows * K, "out too small");
+    const at::cuda::CUDAGuard guard(raw.device());
+    const int rc = launch_dequant_f16(raw.data_ptr(), (int)qtype, (int)rows, (int)K,
+                                      reinterpret_cast<__half*>(out.data_ptr()), cur_stream());
+    TORCH_CHECK(rc == 0, "dequant_f16 failed: rc=", rc);
+  });
   m.def("gemm_with_add", [](const GemmResult& g, Tensor add) {
     CHECK_DT(add, at::kFloat);
     TORCH_CHECK(add.size(-1) == g.g.rows && add.stride(-1) == 1, "add must be [T, rows]");

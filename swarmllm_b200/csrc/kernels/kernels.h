@@ -164,6 +164,9 @@ int launch_tree_rank(const float* logits, int rows, int V, int stride, int k, fl
 int launch_flag_wait(const void* flags, int world, int* ctl, int slot, int* status, int code,
                      cudaStream_t s);
 
+// GGML blocks -> fp16 [rows][K] (qmatmul_simt.cu); quantized types only.
+int launch_dequant_f16(const void* w, int type, int rows, int K, __half* out, cudaStream_t s);
+
 // ---- LoRA (lora.cu) -----------------------------------------------------------
 int launch_lora(const __half* x, int x_stride, int K, const int32_t* ids, int T, const __half* A,
                 const __half* B, const float* scale, int R, int rows, float* u, float* delta,

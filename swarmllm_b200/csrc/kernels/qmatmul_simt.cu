@@ -154,9 +154,52 @@ static void dispatch_t(const uint8_t* w, int rows, int K, const __half* x, int x
   }
 }
 
+// GGML blocks -> fp16 [rows][K], two values per thread (the prefill path of
+// quantized types without a tensor-core kernel of their own: dequantize once,
+// then the dense tcgen05 GEMM).  Memory-bound; the block header re-reads hit L1.
+template <int TYPE>
+__global__ void dequant_f16_kernel(const uint8_t* __restrict__ w, int rows, int K,
+                                   __half* __restrict__ out) {
+  const int BV = ggml_block_values(TYPE), BB = ggml_block_bytes(TYPE);
+  const size_t n2 = (size_t)rows * K / 2;
+  for (size_t p = blockIdx.x * (size_t)blockDim.x + threadIdx.x; p < n2;
+       p += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = 2 * p;
+    const int r = (int)(e / K), k = (int)(e - (size_t)r * K);
+    const uint8_t* blk = w + ((size_t)r * (K / BV) + k / BV) * BB;
+    const int i = k % BV;
+    const float v0 = dequant_one(TYPE, blk, i), v1 = dequant_one(TYPE, blk, i + 1);
+    reinterpret_cast<__half2*>(out)[p] = __floats2half2_rn(v0, v1);
+  }
+}
+
+template <int TYPE>
+static void dequant_t(const uint8_t* w, int rows, int K, __half* out, cudaStream_t s) {
+  const size_t n2 = (size_t)rows * K / 2;
+  const int blocks = (int)((n2 + 255) / 256 < 65536 ? (n2 + 255) / 256 : 65536);
+  dequant_f16_kernel<TYPE><<<blocks, 256, 0, s>>>(w, rows, K, out);
+}
+
 }  // namespace swarm
 
 using namespace swarm;
+
+int launch_dequant_f16(const void* w, int type, int rows, int K, __half* out, cudaStream_t s) {
+  if (rows <= 0 || K <= 0) return 0;
+  if (K % 2 != 0 || K % ggml_block_values(type) != 0) return -1;
+  const uint8_t* wb = (const uint8_t*)w;
+  switch (type) {
+    case GGML_Q4_0: dequant_t<GGML_Q4_0>(wb, rows, K, out, s); break;
+    case GGML_Q8_0: dequant_t<GGML_Q8_0>(wb, rows, K, out, s); break;
+    case GGML_Q4_K: dequant_t<GGML_Q4_K>(wb, rows, K, out, s); break;
+    case GGML_Q6_K: dequant_t<GGML_Q6_K>(wb, rows, K, out, s); break;
+    case GGML_IQ4_NL: dequant_t<GGML_IQ4_NL>(wb, rows, K, out, s); break;
+    case GGML_IQ4_XS: dequant_t<GGML_IQ4_XS>(wb, rows, K, out, s); break;
+    case GGML_MXFP4: dequant_t<GGML_MXFP4>(wb, rows, K, out, s); break;
+    default: return -2;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -3;
+}
 
 int launch_qmatmul_simt(const void* w, int type, int rows, int K, const __half* x,
                         int x_stride, int T, float* out, int out_stride, cudaStream_t s) {

@@ -34,6 +34,23 @@ def stream_k_floats(max_tokens: int, rows: int, num_sms: int) -> int:
     return need
 
 
+# Quantized types without a tensor-core kernel of their own take the
+# dequantize + dense GEMM path from this many tokens on (prefill).
+DEQUANT_MIN_TOKENS = 64
+_DEQUANT_TYPES = (Q.Q4_0, Q.Q8_0, Q.Q4_K, Q.Q6_K, Q.IQ4_NL, Q.IQ4_XS, Q.MXFP4)
+_DQ_SCRATCH: dict = {}
+
+
+def _dequant_scratch(device, n: int) -> torch.Tensor:
+    """fp16 scratch of at least n values per device, shared by every layer
+    (grows outside CUDA-graph capture only; prefill is not captured)."""
+    key = str(device)
+    buf = _DQ_SCRATCH.get(key)
+    if buf is None or buf.numel() < n:
+        buf = _DQ_SCRATCH[key] = torch.empty(n, dtype=torch.float16, device=device)
+    return buf
+
+
 class GemmWorkspace:
     """Scratch shared by every GEMM of one forward: the stream-K partial
     buffer, a dense fallback buffer and the kernel status word."""
@@ -120,6 +137,13 @@ class QLinear:
             return C().qgemm_q4k_tc(self.packed, self.rows, self.K, x, ws.ws, ws.status, ws.num_sms)
         if self.kind == "dense":
             return C().dense_gemm_tc(self.w16, x, ws.ws, ws.status, ws.num_sms)
+        if (T >= DEQUANT_MIN_TOKENS and self.qtype in _DEQUANT_TYPES and self.K % 8 == 0
+                and not torch.cuda.is_current_stream_capturing()):
+            # prefill-sized batch: dequantize once to fp16 and run the dense
+            # tensor-core GEMM (the CUDA-core kernel re-reads the blocks per 8 tokens)
+            w16 = _dequant_scratch(self.device, self.rows * self.K)[: self.rows * self.K]
+            C().dequant_f16(self.raw, self.qtype, self.rows, self.K, w16)
+            return C().dense_gemm_tc(w16.view(self.rows, self.K), x, ws.ws, ws.status, ws.num_sms)
         if out is None:
             out = ws.dense(T * self.rows)[: T * self.rows].view(T, self.rows)
         return C().qmatmul_simt(self.raw, self.qtype, self.rows, self.K, x, out)

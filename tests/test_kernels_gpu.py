@@ -92,6 +92,27 @@ def test_qgemv_q4k_strided(rows, K, T):
     assert rel_err(out.cpu(), ref) < 3e-3
 
 
+@pytest.mark.parametrize("qt", [Q.Q4_0, Q.Q8_0, Q.Q6_K, Q.IQ4_NL, Q.IQ4_XS, Q.MXFP4])
+def test_prefill_dequant_dense_path(qt):
+    """Prefill-sized batches of types without their own tensor-core kernel:
+    dequantize to fp16, then the dense tcgen05 GEMM."""
+    from swarmllm_b200.ops.linear import DEQUANT_MIN_TOKENS, GemmWorkspace, QLinear
+    rows, K, T = 640, 1024, max(DEQUANT_MIN_TOKENS, 100)
+    rng = np.random.default_rng(qt)
+    w = rng.standard_normal((rows, K), dtype=np.float32) * 0.02
+    b = Q.quantize(w, qt)
+    wd = torch.from_numpy(Q.dequantize(b, qt).reshape(rows, K))
+    x = _x(T, K, seed=5)
+    ref = x.float() @ wd.T
+    lin = QLinear(b, qt, rows, K, DEV)
+    ws = GemmWorkspace(DEV, T, rows)
+    g = lin(x.to(DEV), ws)
+    out = _dense_from(g, T, rows)
+    torch.cuda.synchronize()
+    ws.check()
+    assert rel_err(out.cpu(), ref) < 3e-3
+
+
 def test_q4k_repack_matches_host():
     rows, K = 256, 512
     rng = np.random.default_rng(3)
