@@ -93,6 +93,47 @@ int BlockManager::add_sequence(int64_t seq_id, const std::vector<int32_t>& token
   return covered;
 }
 
+std::vector<int32_t> BlockManager::cached_prefix_pages(const std::vector<int32_t>& tokens) const {
+  std::vector<int32_t> out;
+  if (!prefix_) return out;
+  uint64_t h = 0;
+  const int full = (int)tokens.size() / page_size_;
+  for (int i = 0; i < full; ++i) {
+    const uint64_t nh = hash_page(h, tokens.data() + (size_t)i * page_size_, page_size_);
+    auto it = hash_to_page_.find(nh);
+    if (it == hash_to_page_.end()) break;
+    out.push_back(it->second);
+    h = nh;
+  }
+  return out;
+}
+
+std::vector<int32_t> BlockManager::import_prefix_pages(const std::vector<int32_t>& tokens,
+                                                       int n_pages) {
+  std::vector<int32_t> out;
+  if (!prefix_) return out;
+  n_pages = std::min(n_pages, (int)tokens.size() / page_size_);
+  uint64_t h = 0;
+  for (int i = 0; i < n_pages; ++i) {
+    const uint64_t nh = hash_page(h, tokens.data() + (size_t)i * page_size_, page_size_);
+    h = nh;
+    if (hash_to_page_.count(nh)) {  // already cached here: keep ours
+      out.push_back(-1);
+      continue;
+    }
+    const int p = alloc_page();
+    if (p < 0) {  // no room: the rest of the chain is not importable
+      out.push_back(-1);
+      break;
+    }
+    page_hash_[p] = nh;
+    hash_to_page_[nh] = p;
+    release_page(p);  // ref 1 -> 0: cached and evictable
+    out.push_back(p);
+  }
+  return out;
+}
+
 int BlockManager::seq_len(int64_t seq_id) const {
   auto it = seqs_.find(seq_id);
   if (it == seqs_.end()) throw std::out_of_range("no such sequence");

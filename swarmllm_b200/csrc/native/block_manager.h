@@ -49,6 +49,17 @@ class BlockManager {
   void fill_block_table(const std::vector<int64_t>& seq_ids, int max_pages, int32_t* out) const;
 
   int64_t prefix_hits() const { return prefix_hit_tokens_; }
+  // Prefix snapshots (export / import of cached KV pages, e.g. across nodes).
+  // Pages of the longest cached chain of full pages of `tokens` (no
+  // references are taken: copy them out before scheduling more work).
+  std::vector<int32_t> cached_prefix_pages(const std::vector<int32_t>& tokens) const;
+  // Make the first n_pages full pages of `tokens` cached: for each page of
+  // the chain not already cached, take a free (or evict an LRU) page and
+  // register its hash; it is left unreferenced in the LRU, as if a finished
+  // request had produced it.  Returns one entry per page: the page to fill
+  // with the KV data, or -1 where the page was already cached (or no page
+  // was available; the chain stops there).
+  std::vector<int32_t> import_prefix_pages(const std::vector<int32_t>& tokens, int n_pages);
   int num_cached_pages() const { return (int)hash_to_page_.size(); }
 
  private:

@@ -44,6 +44,11 @@ PYBIND11_MODULE(_native, m) {
              b.fill_block_table(ids, max_pages, a.mutable_data());
              return a;
            })
+      .def("cached_prefix_pages",
+           [](const BlockManager& b, const std::vector<int32_t>& t) { return to_np(b.cached_prefix_pages(t)); })
+      .def("import_prefix_pages", [](BlockManager& b, const std::vector<int32_t>& t, int n) {
+        return to_np(b.import_prefix_pages(t, n));
+      })
       .def_property_readonly("prefix_hit_tokens", &BlockManager::prefix_hits)
       .def_property_readonly("num_cached_pages", &BlockManager::num_cached_pages);
 

@@ -140,6 +140,17 @@ class LLMEngine:
         return int(max(64, min(budget // per_page, need)))
 
     # ------------------------------------------------------------------ API
+    def export_prefix(self, tokens):
+        """PrefixSnapshot of the cached KV pages of `tokens` (engine/prefix_share.py)."""
+        from .prefix_share import export_prefix
+        return export_prefix(self, tokens)
+
+    def import_prefix(self, snapshot) -> int:
+        """Load a PrefixSnapshot into this engine's prefix cache; returns the
+        number of tokens newly cached."""
+        from .prefix_share import import_prefix
+        return import_prefix(self, snapshot)
+
     def load_lora(self, adapter, name: str | None = None) -> str:
         """Register a LoRA adapter (a LoraAdapter or a LoRA GGUF path) for
         requests to select by name."""

@@ -13,6 +13,7 @@ src/api/openai/streaming.rs:1431, src/api/anthropic/):
   POST /v1/embeddings          (mean-pooled, L2-normalised input embeddings)
   GET  /v1/models              (the base model and every loaded LoRA adapter)
   GET  /health, /health/ready, /metrics (Prometheus), /api/status, /v1/status
+  POST /api/prefix/export, /api/prefix/import   (prefix-KV snapshots, engine/prefix_share.py)
   WS   /api/admin/ws           (status feed, one JSON message a second)
 
 Auth, CORS, rate limits, security headers and the body-size cap are one ASGI
@@ -60,6 +61,7 @@ class AsyncEngine:
         self.metrics = metrics or Metrics()
         self._in: queue.Queue = queue.Queue()
         self._abort: queue.Queue = queue.Queue()
+        self._calls: queue.Queue = queue.Queue()
         self._subs: dict[int, _Sub] = {}
         self._ids = itertools.count(1)
         self._wake = threading.Event()
@@ -79,6 +81,14 @@ class AsyncEngine:
     def abort(self, rid: int):
         self._abort.put(rid)
         self._wake.set()
+
+    async def call(self, fn):
+        """Run fn(engine) on the engine thread between steps; returns its result."""
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        self._calls.put((fn, fut, loop))
+        self._wake.set()
+        return await fut
 
     def shutdown(self):
         self._stop = True
@@ -108,6 +118,16 @@ class AsyncEngine:
                 if rid in self._subs:
                     eng.abort(rid)
                     self._finish(rid, "aborted")
+            while True:
+                try:
+                    fn, fut, loop = self._calls.get_nowait()
+                except queue.Empty:
+                    break
+                try:
+                    r = fn(eng)
+                    loop.call_soon_threadsafe(lambda f=fut, v=r: f.done() or f.set_result(v))
+                except Exception as e:
+                    loop.call_soon_threadsafe(lambda f=fut, x=e: f.done() or f.set_exception(x))
             if not eng.has_work():
                 self._wake.wait(0.05)
                 self._wake.clear()
@@ -559,6 +579,36 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
         e = aengine.engine
         aengine.metrics.set_kv(e.bm.num_free(), e.bm.num_pages)
         return PlainTextResponse(aengine.metrics.render(), media_type="text/plain; version=0.0.4")
+
+    # ------------------------------------------------------------------ prefix KV snapshots
+    @app.post("/api/prefix/export")
+    async def prefix_export(request: Request):
+        """Body {"prompt": text} or {"tokens": [...]}: the cached KV pages of that
+        prefix as a snapshot (application/octet-stream; 204 if none cached)."""
+        from fastapi.responses import Response
+        body = await body_of(request)
+        toks = body.get("tokens")
+        if toks is None:
+            toks = tokenizer.encode(body.get("prompt", ""))
+        snap = await aengine.call(lambda e: e.export_prefix(list(toks)))
+        if snap is None:
+            return Response(status_code=204)
+        return Response(snap.to_bytes(), media_type="application/octet-stream",
+                        headers={"x-swarmllm-prefix-tokens": str(len(snap.tokens))})
+
+    @app.post("/api/prefix/import")
+    async def prefix_import(request: Request):
+        from ..engine.prefix_share import PrefixSnapshot
+        raw = await request.body()
+        try:
+            snap = PrefixSnapshot.from_bytes(raw)
+        except (ValueError, KeyError) as e:
+            raise ApiError(400, f"bad snapshot: {e}")
+        try:
+            n = await aengine.call(lambda e: e.import_prefix(snap))
+        except (ValueError, RuntimeError) as e:
+            raise ApiError(400, str(e))
+        return {"imported_tokens": n, "snapshot_tokens": len(snap.tokens)}
 
     @app.websocket("/api/admin/ws")
     async def ws_feed(ws: WebSocket):

@@ -84,3 +84,30 @@ def test_tokenizers_roundtrip():
     ids = tk.encode("hello world", add_bos=False)
     assert tk.decode(ids) == "hello world"
     assert toks.index("hello") in ids
+
+
+def test_prefix_snapshot_over_http(client):
+    """Export the cached prefix of a completed prompt, then import it into a
+    second server: the second server caches the pages."""
+    from fastapi.testclient import TestClient
+
+    from swarmllm_b200.engine import EngineConfig, LLMEngine
+    from swarmllm_b200.models.config import tiny_llama
+    from swarmllm_b200.serve.api import AsyncEngine, create_app
+    from swarmllm_b200.serve.tokenizer import ByteTokenizer
+    ids = list(range(5, 5 + 40))
+    r = client.post("/v1/completions", json={"prompt": ids, "max_tokens": 2, "temperature": 0})
+    assert r.status_code == 200
+    r = client.post("/api/prefix/export", json={"tokens": ids})
+    assert r.status_code == 200 and r.headers["x-swarmllm-prefix-tokens"] == "32"
+    snap = r.content
+    assert client.post("/api/prefix/import", content=snap).json()["imported_tokens"] == 0
+    assert client.post("/api/prefix/import", content=b"garbage").status_code == 400
+    cfg = tiny_llama()
+    eng = LLMEngine.from_config(cfg, "cpu", EngineConfig(max_model_len=512, max_running=4,
+                                                        max_step_tokens=512, prefill_chunk=256))
+    ae = AsyncEngine(eng)
+    with TestClient(create_app(ae, ByteTokenizer(cfg.vocab), "tiny-llama", max_model_len=512)) as c2:
+        assert c2.post("/api/prefix/import", content=snap).json()["imported_tokens"] == 32
+        assert c2.post("/api/prefix/export", json={"tokens": [9, 9, 9]}).status_code == 204
+    ae.shutdown()
