@@ -39,6 +39,8 @@ def _engine(args):
         eng = LLMEngine.from_config(preset(args.model), dev, ecfg, seed=args.seed)
     for name, path in loras:
         eng.load_lora(path, name)
+    if getattr(args, "mmproj", None):
+        eng.load_vision(args.mmproj)
     return eng
 
 
@@ -65,6 +67,7 @@ def main(argv=None):
         s.add_argument("--max-model-len", type=int, default=0)
         s.add_argument("--lora", action="append", default=[], metavar="NAME=PATH",
                        help="LoRA adapter GGUF; requests select it with model NAME")
+        s.add_argument("--mmproj", default=None, help="image encoder GGUF (vision input)")
         if name == "serve":
             s.add_argument("--host", default="0.0.0.0")
             s.add_argument("--port", type=int, default=8800)

@@ -67,6 +67,8 @@ class LLMEngine:
         n_kv_layers = getattr(model, "n_kv_layers", model.hi - model.lo)
         self.lora_of: dict[int, int] = {}
         self.lora_names: list[str] = []
+        self.images: dict[int, list] = {}   # request id -> [(first position, image rows)]
+        self.vision = None
         if ecfg.max_loras and self.device.type == "cuda":
             model.enable_lora(ecfg.max_loras, ecfg.max_lora_rank)
         elif ecfg.max_loras:
@@ -84,6 +86,7 @@ class LLMEngine:
                                     ecfg.max_model_len, ecfg.graph_sizes, ecfg.cuda_graphs,
                                     trash_page=pages)
             self.runner.lora_of = self.lora_of if ecfg.max_loras else None
+            self.runner.images = self.images
             if ecfg.cuda_graphs:
                 self.runner.capture_graphs()
         else:
@@ -95,6 +98,7 @@ class LLMEngine:
             self.bm = N.BlockManager(pages, ps, ecfg.prefix_cache)
             self.runner = CpuRunner(model, self.kv, ecfg.max_model_len, ecfg.max_running)
             self.runner.lora_of = self.lora_of if ecfg.max_loras else None
+            self.runner.images = self.images
         self.sched = N.Scheduler(self.bm, ecfg.max_step_tokens, ecfg.max_running, ecfg.prefill_chunk)
         self.params: dict[int, SamplingParams] = {}
         self.traces: dict[int, RequestTrace] = {}
@@ -169,10 +173,40 @@ class LLMEngine:
             self.lora_names.append(adapter.name)
         return adapter.name
 
+    def load_vision(self, mmproj_path: str):
+        """Image encoder for prompts with images (an mmproj GGUF)."""
+        from ..models.vision import VisionEncoder
+        self.vision = VisionEncoder.from_gguf(mmproj_path, self.cfg.hidden, device=self.device)
+        return self.vision
+
+    def _splice_images(self, prompt_ids, images):
+        """Each IMAGE_TOKEN in the prompt becomes the image's rows: placeholder
+        ids (derived from the rows, for the prefix cache) whose embeddings the
+        runner replaces with the encoder's rows."""
+        from ..models.vision import IMAGE_TOKEN, image_placeholders
+        if self.vision is None:
+            raise RuntimeError("no image encoder loaded (load_vision / --mmproj)")
+        if sum(1 for t in prompt_ids if t == IMAGE_TOKEN) != len(images):
+            raise ValueError("the prompt must carry one image marker per image")
+        ids, spans, k = [], [], 0
+        for t in prompt_ids:
+            if t == IMAGE_TOKEN:
+                rows = self.vision.encode([images[k]])
+                k += 1
+                spans.append((len(ids), rows.to(self.device)))
+                ids.extend(image_placeholders(rows, rows.shape[0], self.cfg.vocab))
+            else:
+                ids.append(int(t))
+        return ids, spans
+
     def add_request(self, prompt_ids, params: SamplingParams | None = None,
-                    request_id: int | None = None, lora: str | None = None) -> int:
+                    request_id: int | None = None, lora: str | None = None,
+                    images=None) -> int:
         params = params or SamplingParams()
         rid = next(self._ids) if request_id is None else request_id
+        if images:
+            prompt_ids, spans = self._splice_images(list(prompt_ids), images)
+            self.images[rid] = spans
         if lora is not None:
             self.lora_of[rid] = self.lora_names.index(lora)
         eos = -1 if params.ignore_eos else params.eos_token_id
@@ -185,6 +219,7 @@ class LLMEngine:
     def abort(self, rid: int):
         self.sched.abort(rid)
         self._free_state(rid)
+        self.images.pop(rid, None)
 
     def _free_state(self, rid: int):
         slots = getattr(self.runner, "slots", None)
@@ -245,6 +280,7 @@ class LLMEngine:
         self.sched.release(rid)
         self._free_state(rid)
         self.lora_of.pop(rid, None)
+        self.images.pop(rid, None)
         self.params.pop(rid, None)
         self.prompt_len.pop(rid, None)
 

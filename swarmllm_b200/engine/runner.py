@@ -71,6 +71,32 @@ def ssm_table(plan, positions, slots: StateSlots) -> np.ndarray:
     return out
 
 
+def image_rows(plan, positions, images: dict):
+    """(rows int32 [n], embeddings [n, hidden]) of this step's rows that fall
+    on an image's span of a prompt (images: request id -> [(first position,
+    rows tensor)]), or None."""
+    if not images:
+        return None
+    rs, pos = np.asarray(plan.row_seq), np.asarray(positions)
+    idx, vals = [], []
+    for si, rid in enumerate(np.asarray(plan.seq_ids)):
+        spans = images.get(int(rid))
+        if not spans:
+            continue
+        rows = np.nonzero(rs == si)[0]
+        if len(rows) == 0:
+            continue
+        p = pos[rows]
+        for p0, data in spans:
+            m = (p >= p0) & (p < p0 + data.shape[0])
+            if m.any():
+                idx.append(rows[m])
+                vals.append(data[torch.as_tensor(p[m] - p0, dtype=torch.int64, device=data.device)])
+    if not idx:
+        return None
+    return np.concatenate(idx).astype(np.int32), torch.cat(vals)
+
+
 def lora_rows(plan, lora_of: dict) -> np.ndarray:
     """int32 [N] adapter index of each token row (-1: none)."""
     per_seq = np.array([lora_of.get(int(s), -1) for s in plan.seq_ids], np.int32)
@@ -124,6 +150,7 @@ class GpuRunner:
         self.use_graphs = use_graphs
         self.graphs: dict[int, tuple] = {}
         self.lora_of = None
+        self.images: dict = {}
         self.d_lora = torch.full((mt,), -1, dtype=torch.int32, device=dev)
         self.h_lora = torch.full((mt,), -1, dtype=torch.int32).pin_memory()
         self.slots = None
@@ -265,6 +292,10 @@ class GpuRunner:
             if grp is not None:
                 b.groups = (torch.from_numpy(grp[0]).to(self.device, non_blocking=True),
                             torch.from_numpy(grp[1]).to(self.device, non_blocking=True), grp[2])
+            ir = image_rows(plan, positions, self.images)
+            if ir is not None:
+                b.embed_rows = torch.from_numpy(ir[0]).to(self.device)
+                b.embed_vals = ir[1].to(self.device)
             logits = self.model.forward(b, self.kv, self.ctx)
             res = self.sampler.sample(logits, params, positions[sample_rows] if S else [])
         self.h_out[:S].copy_(res, non_blocking=True)
@@ -291,6 +322,10 @@ class CpuRunner:
             b.ssm_seqs = torch.from_numpy(ssm_table(plan, positions, self.slots))
         if getattr(self, "lora_of", None) is not None:
             b.lora_ids = torch.from_numpy(lora_rows(plan, self.lora_of))
+        ir = image_rows(plan, positions, getattr(self, "images", None))
+        if ir is not None:
+            b.embed_rows = torch.from_numpy(ir[0])
+            b.embed_vals = ir[1].cpu()
         return self.model.forward(b, self.kv, None, h_in), positions, sample_rows
 
     def run(self, plan, block_manager, params: list[SamplingParams]) -> np.ndarray:

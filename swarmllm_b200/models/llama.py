@@ -50,6 +50,8 @@ class StepBatch:
     ssm_seqs: torch.Tensor | None = None    # int32 [S, 4] (row0, nrows, state slot, pos0): linear attention
     ssm_max_rows: int = 1                   # host hint: most rows of one sequence in this step
     lora_ids: torch.Tensor | None = None    # int32 [N] adapter index per row (-1: none)
+    embed_rows: torch.Tensor | None = None  # int32 [n] rows whose embedding is given (images)
+    embed_vals: torch.Tensor | None = None  # [n, hidden] those rows' embeddings
 
 
 def _f32(t: torch.Tensor, qt: int, shape) -> torch.Tensor:
@@ -338,6 +340,8 @@ class LlamaGPU:
         h = ctx.h[:N]
         if self.first:
             C().embed_gather(self.embd, self.embd_type, H, b.tokens, h)
+            if b.embed_rows is not None:  # image rows spliced into the prompt
+                h.index_copy_(0, b.embed_rows.long(), b.embed_vals.to(h.dtype))
         elif h_in is not None and h_in.data_ptr() != h.data_ptr():
             h.copy_(h_in)
         x = ctx.x[:N]
@@ -675,6 +679,8 @@ class LlamaCPU:
         nq, nkv, d = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         rep = nq // nkv
         h = self.embd[b.tokens.long()].clone() if self.first else h_in.to(self.dtype).clone()
+        if self.first and b.embed_rows is not None:  # image rows spliced into the prompt
+            h.index_copy_(0, b.embed_rows.long(), b.embed_vals.to(h.dtype))
         ps = kv.page_size
         slots = b.slots.long()
         pages, offs = slots // ps, slots % ps

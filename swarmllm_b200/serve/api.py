@@ -53,6 +53,7 @@ class _Sub:
     q: asyncio.Queue
     loop: asyncio.AbstractEventLoop
     lora: str | None = None
+    images: list | None = None
 
 
 class AsyncEngine:
@@ -70,11 +71,12 @@ class AsyncEngine:
         self._t = threading.Thread(target=self._run, daemon=True, name="engine")
         self._t.start()
 
-    def submit(self, prompt_ids, params: SamplingParams,
-               lora: str | None = None) -> tuple[int, asyncio.Queue]:
+    def submit(self, prompt_ids, params: SamplingParams, lora: str | None = None,
+               images=None) -> tuple[int, asyncio.Queue]:
         rid = next(self._ids)
         q: asyncio.Queue = asyncio.Queue()
-        self._in.put(_Sub(rid, list(prompt_ids), params, q, asyncio.get_running_loop(), lora))
+        self._in.put(_Sub(rid, list(prompt_ids), params, q, asyncio.get_running_loop(), lora,
+                          images))
         self._wake.set()
         return rid, q
 
@@ -105,6 +107,8 @@ class AsyncEngine:
                     break
                 try:
                     kw = {"lora": s.lora} if s.lora else {}
+                    if s.images:
+                        kw["images"] = s.images
                     eng.add_request(s.prompt, s.params, request_id=s.rid, **kw)
                     self._subs[s.rid] = s
                     self.metrics.requests_started()
@@ -209,6 +213,11 @@ class Serving:
         return [self.model_name] + [f"{self.model_name}:{n}" for n in
                                     getattr(self.ae.engine, "lora_names", None) or []]
 
+    def prompt_len(self, ids, images) -> int:
+        """Positions the prompt takes once each image marker is its rows."""
+        v = getattr(self.ae.engine, "vision", None)
+        return len(ids) + (len(images) * (v.rows_per_image - 1) if images and v else 0)
+
     def params(self, body: dict, n_prompt: int) -> SamplingParams:
         mt = body.get("max_tokens", body.get("max_completion_tokens", body.get("max_output_tokens")))
         if mt is None:
@@ -231,9 +240,11 @@ class Serving:
         return [st] if isinstance(st, str) else list(st)
 
     def prepare(self, messages: list[dict], tools: list[ToolSpec] | None = None, tool_choice=None,
-                response_format: dict | None = None) -> tuple[list[int], list[ToolSpec]]:
-        """Token ids of the rendered conversation; the tools that stay active."""
-        msgs = [self._flatten(m) for m in messages]
+                response_format: dict | None = None) -> tuple[list[int], list[ToolSpec], list]:
+        """Token ids of the rendered conversation (IMAGE_TOKEN where an image
+        goes), the tools that stay active, and the images (encoded bytes)."""
+        images: list = []
+        msgs = [self._flatten(m, images) for m in messages]
         extra = []
         if tools and not tool_choice_forbids(tool_choice):
             extra.append(format_tool_prompt(tools, tool_choice))
@@ -251,13 +262,24 @@ class Serving:
                 msgs[0] = {"role": "system", "content": msgs[0]["content"] + "\n\n" + text}
             else:
                 msgs.insert(0, {"role": "system", "content": text})
-        ids = self.tok.encode(render(msgs, self.arch, self.template))
-        return ids, tools
+        text = render(msgs, self.arch, self.template)
+        if not images:
+            return self.tok.encode(text), tools, images
+        if getattr(self.ae.engine, "vision", None) is None:
+            raise ApiError(400, "this model takes no image input (start the server with --mmproj)")
+        from ..models.vision import IMAGE_TOKEN, MEDIA_MARKER
+        pieces = text.split(MEDIA_MARKER)
+        ids = self.tok.encode(pieces[0])
+        for piece in pieces[1:]:
+            ids.append(IMAGE_TOKEN)
+            ids += self.tok.encode(piece, add_bos=False)
+        return ids, tools, images
 
     @staticmethod
-    def _flatten(m: dict) -> dict:
+    def _flatten(m: dict, images: list | None = None) -> dict:
         """One message with plain-text content: assistant tool calls become the
-        JSON shape the tool prompt asks for; tool results become text."""
+        JSON shape the tool prompt asks for; tool results become text; images
+        (inline data only) become a marker, their bytes appended to `images`."""
         role = m.get("role", "user")
         c = m.get("content", "")
         if isinstance(c, list):
@@ -266,7 +288,13 @@ class Serving:
                 if not isinstance(p, dict):
                     continue
                 t = p.get("type")
-                if t in ("text", "input_text", "output_text"):
+                if t in ("image_url", "image", "input_image"):
+                    from ..models.vision import MEDIA_MARKER
+                    if images is None:
+                        raise ApiError(400, "images are not accepted here")
+                    images.append(_image_bytes(p))
+                    parts.append(MEDIA_MARKER)
+                elif t in ("text", "input_text", "output_text"):
                     parts.append(p.get("text", ""))
                 elif t == "tool_use":
                     parts.append(json.dumps({"tool_calls": [{"name": p.get("name"),
@@ -288,11 +316,11 @@ class Serving:
 
     # ---------------------------------------------------------------- generation
     async def stream(self, ids, sp: SamplingParams, stops: list[str], tools=None,
-                     lora: str | None = None):
+                     lora: str | None = None, images=None):
         """Async generator of events:
              ("text", delta)          content to show now
              ("done", Result)         at the end (calls parsed, counts, trace)."""
-        rid, q = self.ae.submit(ids, sp, lora)
+        rid, q = self.ae.submit(ids, sp, lora, images)
         toks: list[int] = []
         text = ""
         sent = 0
@@ -303,7 +331,8 @@ class Serving:
                     raise ApiError(500, msg[1], "server_error")
                 if msg[0] == "done":
                     fin = "length" if len(toks) >= sp.max_tokens else "stop"
-                    yield self._finish(text, sent, tools, fin, len(ids), len(toks), msg[2])
+                    yield self._finish(text, sent, tools, fin, self.prompt_len(ids, images), len(toks),
+                                       msg[2])
                     return
                 toks.append(msg[1])
                 if msg[1] == self.eos and not sp.ignore_eos:
@@ -313,7 +342,8 @@ class Serving:
                 if hit >= 0:
                     text = text[:hit]
                     self.ae.abort(rid)
-                    yield self._finish(text, sent, tools, "stop", len(ids), len(toks), None)
+                    yield self._finish(text, sent, tools, "stop", self.prompt_len(ids, images),
+                                       len(toks), None)
                     return
                 safe = content_prefix_len(text) if tools else len(text)
                 if safe > sent:
@@ -332,11 +362,32 @@ class Serving:
         r.rest = r.text[sent:] if len(r.text) > sent else ""
         return ("done", r)
 
-    async def run(self, ids, sp, stops, tools=None, lora=None) -> Result:
-        async for ev in self.stream(ids, sp, stops, tools, lora):
+    async def run(self, ids, sp, stops, tools=None, lora=None, images=None) -> Result:
+        async for ev in self.stream(ids, sp, stops, tools, lora, images):
             if ev[0] == "done":
                 return ev[1]
         raise ApiError(500, "generation ended without a result", "server_error")
+
+
+def _image_bytes(part: dict) -> bytes:
+    """Encoded image bytes of an OpenAI (image_url / input_image data URL) or
+    Anthropic (base64 source) content part.  No fetching: inline data only."""
+    import base64
+    src = part.get("source")
+    if isinstance(src, dict):                      # Anthropic
+        if src.get("type") != "base64":
+            raise ApiError(400, "only base64 image sources are accepted")
+        data = src.get("data", "")
+    else:
+        url = part.get("image_url")
+        url = url.get("url") if isinstance(url, dict) else url
+        if not isinstance(url, str) or not url.startswith("data:") or "," not in url:
+            raise ApiError(400, "images must be data: URLs (this server fetches nothing)")
+        data = url.split(",", 1)[1]
+    try:
+        return base64.b64decode(data, validate=False)
+    except ValueError:
+        raise ApiError(400, "image data is not base64")
 
 
 def _loads_or(v):
@@ -395,8 +446,8 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
             tools = tools_from_openai(body.get("tools"))
         except ValueError as e:
             raise ApiError(400, str(e))
-        ids, tools = S.prepare(msgs, tools, body.get("tool_choice"), body.get("response_format"))
-        sp = S.params(body, len(ids))
+        ids, tools, images = S.prepare(msgs, tools, body.get("tool_choice"), body.get("response_format"))
+        sp = S.params(body, S.prompt_len(ids, images))
         lora = S.lora_of(body)
         stops = S.stops(body)
         cid = "chatcmpl-" + uuid.uuid4().hex[:24]
@@ -410,7 +461,7 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
         if body.get("stream"):
             async def gen():
                 yield chunk({"role": "assistant"})
-                async for ev in S.stream(ids, sp, stops, tools, lora):
+                async for ev in S.stream(ids, sp, stops, tools, lora, images):
                     if ev[0] == "text":
                         yield chunk({"content": ev[1]})
                         continue
@@ -428,7 +479,7 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
                                              "total_tokens": r.n_prompt + r.n_out}})
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
-        r = await S.run(ids, sp, stops, tools, lora)
+        r = await S.run(ids, sp, stops, tools, lora, images)
         msg = {"role": "assistant", "content": r.text if (r.text or not r.calls) else None}
         if r.calls:
             msg["tool_calls"] = [c.openai() for c in r.calls]
@@ -477,8 +528,8 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
         if sysmsg:
             msgs = [{"role": "system", "content": sysmsg if isinstance(sysmsg, str) else
                      "".join(b.get("text", "") for b in sysmsg)}] + msgs
-        ids, tools = S.prepare(msgs, tools_from_anthropic(body.get("tools")), body.get("tool_choice"))
-        sp = S.params(body, len(ids))
+        ids, tools, images = S.prepare(msgs, tools_from_anthropic(body.get("tools")), body.get("tool_choice"))
+        sp = S.params(body, S.prompt_len(ids, images))
         lora = S.lora_of(body)
         mid = "msg_" + uuid.uuid4().hex[:24]
         stop_of = {"length": "max_tokens", "tool_calls": "tool_use", "stop": "end_turn"}
@@ -491,7 +542,7 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
                     "content": [], "stop_reason": None,
                     "usage": {"input_tokens": len(ids), "output_tokens": 0}}})
                 opened = False
-                async for e in S.stream(ids, sp, S.stops(body), tools, lora):
+                async for e in S.stream(ids, sp, S.stops(body), tools, lora, images):
                     delta = e[1] if e[0] == "text" else e[1].rest
                     if delta:
                         if not opened:
@@ -521,7 +572,7 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
                                                "usage": {"output_tokens": r.n_out}})
                 yield ev("message_stop", {"type": "message_stop"})
             return StreamingResponse(gen(), media_type="text/event-stream")
-        r = await S.run(ids, sp, S.stops(body), tools, lora)
+        r = await S.run(ids, sp, S.stops(body), tools, lora, images)
         content = ([{"type": "text", "text": r.text}] if r.text or not r.calls else []) + \
             [c.anthropic() for c in r.calls]
         return {"id": mid, "type": "message", "role": "assistant", "model": body.get("model", model_name),

@@ -102,7 +102,7 @@ def register(app, S):
             msgs.insert(0, {"role": "system", "content": str(args["system"])})
         body = {"max_tokens": args.get("max_tokens", 256), "temperature": args.get("temperature", 0.0),
                 "model": model}
-        ids, _ = S.prepare(msgs)
+        ids, _, _ = S.prepare(msgs)
         sp = S.params(body, len(ids))
         r = await S.run(ids, sp, [], None, S.lora_of(body))
         return {"model": model or S.model_name, "text": r.text, "finish_reason": r.finish,

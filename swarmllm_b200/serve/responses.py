@@ -161,8 +161,11 @@ def messages_of(items: list[dict]) -> list[dict]:
         t = it["type"]
         if t == "message":
             role = it.get("role", "user")
+            c = it.get("content")
+            has_image = isinstance(c, list) and any(isinstance(p, dict) and p.get("type") == "input_image"
+                                                    for p in c)
             msgs.append({"role": "system" if role == "developer" else role,
-                         "content": _item_text(it.get("content"))})
+                         "content": c if has_image else _item_text(c)})
         elif t == "function_call":
             msgs.append({"role": "assistant", "content": "", "tool_calls": [
                 {"id": it.get("call_id"), "function": {"name": it.get("name"),
@@ -189,7 +192,8 @@ def register(app, S, store_path: str | None = None):
     def sse(ev: dict) -> str:
         return f"event: {ev['type']}\ndata: {json.dumps(ev)}\n\n"
 
-    async def produce(obj: dict, ids, sp, stops, tools, lora, items, convo, persist: bool):
+    async def produce(obj: dict, ids, sp, stops, tools, lora, items, convo, persist: bool,
+                      images=None):
         """The typed event sequence of one generation; stores the result."""
         seq = [0]
 
@@ -203,7 +207,7 @@ def register(app, S, store_path: str | None = None):
         opened = False
         text = ""
         try:
-            async for e in S.stream(ids, sp, stops, tools, lora):
+            async for e in S.stream(ids, sp, stops, tools, lora, images):
                 delta = e[1] if e[0] == "text" else e[1].rest
                 if delta or (e[0] == "done" and not opened and not e[1].calls):
                     if not opened:
@@ -299,8 +303,8 @@ def register(app, S, store_path: str | None = None):
         fmt = (body.get("text") or {}).get("format")
         if fmt and fmt.get("type") == "json_schema":
             fmt = {"type": "json_schema", "json_schema": {"schema": fmt.get("schema")}}
-        ids, tools = S.prepare(msgs, tools, body.get("tool_choice"), fmt)
-        sp = S.params(body, len(ids))
+        ids, tools, images = S.prepare(msgs, tools, body.get("tool_choice"), fmt)
+        sp = S.params(body, S.prompt_len(ids, images))
         lora = S.lora_of(body)
         persist = body.get("store", True) is not False
         background, stream = bool(body.get("background")), bool(body.get("stream"))
@@ -313,7 +317,7 @@ def register(app, S, store_path: str | None = None):
                "max_output_tokens": sp.max_tokens, "temperature": sp.temperature, "top_p": sp.top_p,
                "tools": body.get("tools") or [], "tool_choice": body.get("tool_choice", "auto"),
                "metadata": body.get("metadata") or {}, "usage": None}
-        gen = produce(obj, ids, sp, S.stops(body), tools, lora, items, convo, persist)
+        gen = produce(obj, ids, sp, S.stops(body), tools, lora, items, convo, persist, images)
 
         if background:
             run = runs[rid] = _Run(obj)
