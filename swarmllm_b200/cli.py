@@ -119,7 +119,8 @@ def main(argv=None):
         tok, tpl = _tokenizer(args, eng)
         serve(eng, tok, eng.cfg.name, args.host, args.port, arch=eng.cfg.arch, chat_template=tpl,
               max_model_len=eng.ecfg.max_model_len, api_key=args.api_key,
-              cors_origins=tuple(args.cors_origin), rpm=args.rpm, store_path=args.response_store)
+              cors_origins=tuple(args.cors_origin), rpm=args.rpm, store_path=args.response_store,
+              config_path=args.config)
         return
     from .engine.sampling import SamplingParams
     if args.cmd == "generate":

@@ -129,7 +129,9 @@ class LLMEngine:
     def from_gguf(cls, path: str, device="cuda:0", ecfg: EngineConfig | None = None):
         from ..models.weights import GgufSource
         src = GgufSource(path)
-        return cls.from_config(src.cfg, device, ecfg, source=src)
+        eng = cls.from_config(src.cfg, device, ecfg, source=src)
+        eng.source_path = path
+        return eng
 
     def _auto_pages(self) -> int:
         free, _ = torch.cuda.mem_get_info(self.device)

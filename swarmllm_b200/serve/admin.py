@@ -1,0 +1,196 @@
+"""Admin API: the node's operational views and run-time controls.
+
+  GET  /api/admin/stats          totals and last-minute rates (tok/s, busy
+                                 fraction, step time, TTFT p50/p99)
+  GET  /api/admin/performance    the same over 10 s / 60 s / 300 s windows
+  GET  /api/admin/config         engine configuration and guard settings
+  PUT  /api/admin/config         change guard settings (rpm, cors_origins,
+                                 max_body) at run time
+  POST /api/admin/config/reload  re-read the TOML config file given at start-up
+                                 and apply its guard settings
+  GET  /api/admin/models         the served model: architecture, size, weight
+                                 types, LoRA adapters, image encoder
+  POST /api/admin/lora           load a LoRA adapter GGUF ({"name", "path"})
+  GET  /api/admin/diagnostics    devices (memory, SMs, clocks), software
+                                 versions, native extensions loaded, KV cache
+  GET  /api/admin/responses      stored /v1/responses ids (newest first)
+  GET  /api/admin/storage        the model's files and their sizes
+
+Every route needs the API key when one is configured (the guards treat
+/api/admin like any other path).  Model download and Hugging Face search are
+not offered: a node here fetches nothing.
+
+Reference behaviour: src/api/admin.rs (stats, config get/update/reload,
+models, diagnostics, performance, responses, storage breakdown;
+routes at src/api/server.rs:274-330).
+"""
+from __future__ import annotations
+
+import os
+import time
+
+from fastapi import Request  # module level: route annotations resolve from globals
+
+
+def register(app, S, settings, config_path: str | None = None):
+    from .api import ApiError
+
+    def engine():
+        return S.ae.engine
+
+    @app.get("/api/admin/stats")
+    async def stats():
+        out = S.ae.metrics.summary(60.0)
+        e = engine()
+        out.update(running=e.sched.num_running, waiting=e.sched.num_waiting,
+                   kv_pages_free=e.bm.num_free(), kv_pages=e.bm.num_pages,
+                   prefix_cache_hit_tokens=e.bm.prefix_hit_tokens, ready=S.ae.ready)
+        return out
+
+    @app.get("/api/admin/performance")
+    async def performance():
+        m = S.ae.metrics
+        return {"windows": {str(int(w)): m.summary(w) for w in (10.0, 60.0, 300.0)}}
+
+    def config_view() -> dict:
+        e = engine()
+        ec = {k: (list(v) if isinstance(v, tuple) else v) for k, v in vars(e.ecfg).items()}
+        return {"engine": ec, "server": settings.public(), "model": e.cfg.name,
+                "config_file": config_path}
+
+    @app.get("/api/admin/config")
+    async def get_config():
+        return config_view()
+
+    def apply(update: dict):
+        bad = set(update) - {"rpm", "cors_origins", "max_body"}
+        if bad:
+            raise ApiError(400, f"not changeable at run time: {sorted(bad)} "
+                                "(engine settings need a restart)")
+        if "rpm" in update:
+            v = int(update["rpm"])
+            if v < 0:
+                raise ApiError(400, "rpm must be >= 0")
+            settings.rpm = v
+        if "cors_origins" in update:
+            o = update["cors_origins"]
+            if not isinstance(o, list) or not all(isinstance(x, str) for x in o):
+                raise ApiError(400, "cors_origins must be a list of strings")
+            settings.cors_origins = tuple(o)
+        if "max_body" in update:
+            v = int(update["max_body"])
+            if v < 1024:
+                raise ApiError(400, "max_body must be at least 1024 bytes")
+            settings.max_body = v
+
+    @app.put("/api/admin/config")
+    async def put_config(request: Request):
+        body = await request.json()
+        if not isinstance(body, dict):
+            raise ApiError(400, "body must be an object")
+        apply(body.get("server", body))
+        return config_view()
+
+    @app.post("/api/admin/config/reload")
+    async def reload_config():
+        if not config_path:
+            raise ApiError(400, "the server was started without a config file")
+        from ..utils.config import load_server_settings
+        try:
+            upd = load_server_settings(config_path)
+        except (OSError, ValueError) as e:
+            raise ApiError(400, f"cannot read {config_path}: {e}")
+        apply(upd)
+        return config_view()
+
+    @app.get("/api/admin/models")
+    async def models():
+        e = engine()
+        cfg = e.cfg
+        m = e.model
+        weight_bytes = 0
+        types: dict = {}
+        for lin in getattr(m, "_linears", lambda: [])():
+            weight_bytes += lin.nbytes
+            types[str(lin.qtype)] = types.get(str(lin.qtype), 0) + 1
+        v = getattr(e, "vision", None)
+        return {"model": cfg.name, "arch": cfg.arch, "layers": cfg.n_layers, "hidden": cfg.hidden,
+                "vocab": cfg.vocab, "params": cfg.param_count(), "linear_weight_bytes": weight_bytes,
+                "linear_types": types, "lora_adapters": list(getattr(e, "lora_names", [])),
+                "lora_slots": e.ecfg.max_loras,
+                "vision": None if v is None else {"projector": v.cfg.projector,
+                                                  "image_size": v.cfg.image_size,
+                                                  "rows_per_image": v.rows_per_image},
+                "ids": S.models()}
+
+    @app.post("/api/admin/lora")
+    async def load_lora(request: Request):
+        body = await request.json()
+        name, path = body.get("name"), body.get("path")
+        if not name or not path:
+            raise ApiError(400, "name and path are required")
+        if not os.path.isfile(path):
+            raise ApiError(404, f"no file {path}")
+        try:
+            n = await S.ae.call(lambda e: e.load_lora(path, name))
+        except (RuntimeError, ValueError) as ex:
+            raise ApiError(400, str(ex))
+        return {"loaded": n, "models": S.models()}
+
+    @app.get("/api/admin/diagnostics")
+    async def diagnostics():
+        import sys
+
+        import torch
+        e = engine()
+        out = {"python": sys.version.split()[0], "torch": torch.__version__,
+               "cuda": torch.version.cuda, "time": time.time()}
+        devs = []
+        if torch.cuda.is_available():
+            for i in range(torch.cuda.device_count()):
+                p = torch.cuda.get_device_properties(i)
+                free, total = torch.cuda.mem_get_info(i)
+                d = {"index": i, "name": p.name, "sms": p.multi_processor_count,
+                     "memory_total_gb": round(total / 2**30, 2), "memory_free_gb": round(free / 2**30, 2)}
+                try:  # read-only NVML queries
+                    import pynvml
+                    pynvml.nvmlInit()
+                    h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                    d["sm_clock_mhz"] = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    d["power_w"] = round(pynvml.nvmlDeviceGetPowerUsage(h) / 1000, 1)
+                    d["temperature_c"] = pynvml.nvmlDeviceGetTemperature(h, pynvml.NVML_TEMPERATURE_GPU)
+                except Exception:
+                    pass
+                devs.append(d)
+        out["devices"] = devs
+        mods = {}
+        for name in ("swarmllm_b200._C", "swarmllm_b200._native"):
+            mod = sys.modules.get(name)
+            mods[name] = getattr(mod, "__file__", None) if mod else None
+        out["native_extensions"] = mods
+        out["kv_cache"] = {"pages": e.bm.num_pages, "page_size": e.bm.page_size,
+                           "free": e.bm.num_free(), "cached_pages": e.bm.num_cached_pages,
+                           "bytes": int(e.kv.data.numel() * e.kv.data.element_size())}
+        out["device"] = str(e.device)
+        return out
+
+    @app.get("/api/admin/responses")
+    async def responses(limit: int = 50):
+        store = getattr(app.state, "response_store", None)
+        if store is None:
+            return {"data": []}
+        with store.lock:
+            rows = store.db.execute("SELECT id, created FROM responses ORDER BY created DESC LIMIT ?",
+                                    (max(1, min(1000, int(limit))),)).fetchall()
+        return {"data": [{"id": r[0], "created": r[1]} for r in rows]}
+
+    @app.get("/api/admin/storage")
+    async def storage():
+        src = getattr(engine(), "source_path", None)
+        files = []
+        if src:
+            paths = [os.path.join(src, f) for f in sorted(os.listdir(src))] if os.path.isdir(src) else [src]
+            for f in paths:
+                if os.path.isfile(f):
+                    files.append({"path": f, "bytes": os.path.getsize(f)})
+        return {"source": src, "files": files, "total_bytes": sum(f["bytes"] for f in files)}

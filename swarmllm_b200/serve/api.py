@@ -14,6 +14,8 @@ src/api/openai/streaming.rs:1431, src/api/anthropic/):
   GET  /v1/models              (the base model and every loaded LoRA adapter)
   GET  /health, /health/ready, /metrics (Prometheus), /api/status, /v1/status
   POST /api/prefix/export, /api/prefix/import   (prefix-KV snapshots, engine/prefix_share.py)
+  /api/admin/*                 (stats, performance, config, models, lora,
+                               diagnostics, responses, storage: serve/admin.py)
   WS   /api/admin/ws           (status feed, one JSON message a second)
 
 Auth, CORS, rate limits, security headers and the body-size cap are one ASGI
@@ -402,12 +404,12 @@ def _loads_or(v):
 def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "llama",
                chat_template: str | None = None, max_model_len: int = 4096,
                api_key: str | None = None, cors_origins=(), rpm: int = 0, port: int = 8800,
-               store_path: str | None = None):
+               store_path: str | None = None, config_path: str | None = None):
     from fastapi import FastAPI
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
-    from . import mcp, responses
-    from .middleware import SecurityMiddleware
+    from . import admin, mcp, responses
+    from .middleware import SecurityMiddleware, ServerSettings
 
     app = FastAPI(title="swarmllm_b200")
     S = Serving(aengine, tokenizer, model_name, arch, chat_template, max_model_len)
@@ -682,10 +684,12 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
             except Exception:
                 pass
 
+    settings = ServerSettings(api_key or None, port, tuple(cors_origins), rpm)
+    app.state.settings = settings
     responses.register(app, S, store_path)
     mcp.register(app, S)
-    app.add_middleware(SecurityMiddleware, api_key=api_key, port=port,
-                       cors_origins=tuple(cors_origins), rpm=rpm)
+    admin.register(app, S, settings, config_path)
+    app.add_middleware(SecurityMiddleware, settings=settings)
     return app
 
 

@@ -23,6 +23,7 @@ import hmac
 import json
 import threading
 import time
+from dataclasses import dataclass
 
 _EXEMPT = ("/health", "/health/ready")
 _LOOPBACK = ("127.0.0.1", "::1", "localhost")
@@ -79,17 +80,46 @@ class RateLimiter:
             del self.buckets[k]
 
 
+@dataclass
+class ServerSettings:
+    """Guard settings the admin API may change at run time (read per request)."""
+    api_key: str | None = None
+    port: int = 8800
+    cors_origins: tuple = ()
+    rpm: int = 0
+    max_body: int = 32 << 20
+
+    def public(self) -> dict:
+        return {"auth_required": bool(self.api_key), "port": self.port,
+                "cors_origins": list(self.cors_origins), "rpm": self.rpm, "max_body": self.max_body}
+
+
 class SecurityMiddleware:
-    def __init__(self, app, api_key: str | None = None, port: int = 8800, cors_origins=(),
-                 rpm: int = 0, max_body: int = 32 << 20):
-        self.app, self.api_key, self.max_body = app, api_key or None, max_body
-        self.origins = {f"http://localhost:{port}", f"http://127.0.0.1:{port}",
-                        f"http://[::1]:{port}", *cors_origins}
-        self.limiter = RateLimiter(rpm)
+    def __init__(self, app, settings: ServerSettings | None = None, api_key: str | None = None,
+                 port: int = 8800, cors_origins=(), rpm: int = 0, max_body: int = 32 << 20):
+        self.app = app
+        self.settings = settings or ServerSettings(api_key or None, port, tuple(cors_origins), rpm,
+                                                   max_body)
+        self.limiter = RateLimiter(self.settings.rpm)
+
+    @property
+    def api_key(self):
+        return self.settings.api_key or None
+
+    @property
+    def max_body(self):
+        return self.settings.max_body
+
+    @property
+    def origins(self):
+        p = self.settings.port
+        return {f"http://localhost:{p}", f"http://127.0.0.1:{p}", f"http://[::1]:{p}",
+                *self.settings.cors_origins}
 
     async def __call__(self, scope, receive, send):
         if scope["type"] not in ("http", "websocket"):
             return await self.app(scope, receive, send)
+        self.limiter.rpm = self.settings.rpm
         path = scope.get("path", "")
         headers = {k.decode("latin-1").lower(): v.decode("latin-1") for k, v in scope.get("headers", [])}
         client = (scope.get("client") or ("?", 0))[0]

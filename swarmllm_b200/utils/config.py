@@ -14,6 +14,9 @@ overrides.  Names kept where the meaning matches:
 
 Environment: SWARMLLM_MAX_MODEL_LEN, SWARMLLM_MAX_RUNNING, SWARMLLM_PREFILL_CHUNK,
 SWARMLLM_KV_PAGES, SWARMLLM_KV_FRACTION, SWARMLLM_PREFIX_CACHE, SWARMLLM_CUDA_GRAPH.
+
+A [server] table (rpm, cors_origins, max_body) holds the request-guard
+settings; the admin API re-reads it on /api/admin/config/reload.
 """
 from __future__ import annotations
 
@@ -63,3 +66,13 @@ def load_engine_config(path: str | None = None, env=None) -> EngineConfig:
     if cfg.max_step_tokens < cfg.prefill_chunk:
         cfg.max_step_tokens = cfg.prefill_chunk
     return cfg
+
+
+def load_server_settings(path: str) -> dict:
+    """Guard settings from a TOML [server] table (rpm, cors_origins, max_body),
+    the ones the admin API can apply at run time."""
+    import tomllib
+    with open(path, "rb") as f:
+        doc = tomllib.load(f)
+    srv = doc.get("server", {})
+    return {k: srv[k] for k in ("rpm", "cors_origins", "max_body") if k in srv}

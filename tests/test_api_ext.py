@@ -350,3 +350,46 @@ def test_status_websocket_feed():
             a, b = ws.receive_json(), ws.receive_json()
         assert a["type"] == "status" and (a["seq"], b["seq"]) == (0, 1)
     ae.shutdown()
+
+
+def test_admin_api(tmp_path):
+    from fastapi.testclient import TestClient
+
+    from swarmllm_b200.engine import EngineConfig, LLMEngine
+    from swarmllm_b200.models.config import tiny_llama
+    from swarmllm_b200.models.lora import LoraAdapter
+    from swarmllm_b200.serve.api import AsyncEngine, create_app
+    from swarmllm_b200.serve.tokenizer import ByteTokenizer
+    cfg = tiny_llama()
+    eng = LLMEngine.from_config(cfg, "cpu", EngineConfig(max_model_len=256, max_running=4,
+                                                        max_step_tokens=256, prefill_chunk=256,
+                                                        max_loras=1))
+    toml = tmp_path / "c.toml"
+    toml.write_text('[server]\nrpm = 77\ncors_origins = ["https://x.example"]\n')
+    ae = AsyncEngine(eng)
+    app = create_app(ae, ByteTokenizer(cfg.vocab), "tiny", max_model_len=256, api_key="k",
+                     config_path=str(toml))
+    h = {"x-api-key": "k"}
+    with TestClient(app) as c:
+        assert c.get("/api/admin/stats").status_code == 401
+        c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 3}, headers=h)
+        st = c.get("/api/admin/stats", headers=h).json()
+        assert st["requests_completed"] >= 1 and st["tokens_generated"] >= 3
+        assert set(c.get("/api/admin/performance", headers=h).json()["windows"]) == {"10", "60", "300"}
+        cf = c.put("/api/admin/config", json={"rpm": 5}, headers=h).json()
+        assert cf["server"]["rpm"] == 5 and cf["engine"]["max_running"] == 4
+        assert c.put("/api/admin/config", json={"max_running": 9}, headers=h).status_code == 400
+        cf = c.post("/api/admin/config/reload", headers=h).json()
+        assert cf["server"]["rpm"] == 77 and cf["server"]["cors_origins"] == ["https://x.example"]
+        pre = c.options("/v1/models", headers={"Origin": "https://x.example"})
+        assert pre.status_code == 204       # the reloaded origin is live
+        p = str(tmp_path / "ad.gguf")
+        LoraAdapter.random(cfg, rank=4, seed=1).write_gguf(p)
+        r = c.post("/api/admin/lora", json={"name": "ad", "path": p}, headers=h)
+        assert r.status_code == 200 and "tiny:ad" in r.json()["models"]
+        m = c.get("/api/admin/models", headers=h).json()
+        assert m["lora_adapters"] == ["ad"] and m["layers"] == cfg.n_layers
+        d = c.get("/api/admin/diagnostics", headers=h).json()
+        assert d["native_extensions"]["swarmllm_b200._native"] and d["kv_cache"]["pages"] > 0
+        assert c.get("/api/admin/responses", headers=h).json()["data"] == []
+    ae.shutdown()
