@@ -1,6 +1,6 @@
 """Standalone cases of the hot kernels, for profiling one kernel at a time:
 
-    python -m swarmllm_b200.utils.kernel_cases {qgemm|qgemv|dense|attn|moe|delta}
+    python -m swarmllm_b200.utils.kernel_cases {qgemm|qgemv|qgemv_o|dense|attn|moe|delta}
 
 Each case builds benchmark-sized operands on cuda:0 (inputs larger than the
 126 MB L2 where memory traffic matters), runs the kernel a few times and
@@ -32,6 +32,13 @@ if which == "qgemm":       # Llama-3.3-70B gate|up at decode batch 32 (264 MB of
 elif which == "qgemv":     # the same weights at decode batch 1 (CUDA-core GEMV path)
     from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
     rows, K, T = 57344, 8192, 1
+    lin = QLinear(rand_q4k(rows, K), Q.Q4_K, rows, K, dev)
+    ws = GemmWorkspace(dev, T, rows)
+    x = torch.randn(T, K, device=dev).half()
+    for _ in range(5): lin(x, ws)
+elif which == "qgemv_o":   # the o projection at decode batch 1 (8192 x 8192, 38 MB)
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    rows, K, T = 8192, 8192, 1
     lin = QLinear(rand_q4k(rows, K), Q.Q4_K, rows, K, dev)
     ws = GemmWorkspace(dev, T, rows)
     x = torch.randn(T, K, device=dev).half()
