@@ -231,7 +231,7 @@ def main():
         from swarmllm_b200.parallel.bench_ep import ep_bench
         return ep_bench(args)
     from swarmllm_b200.parallel.bench_pp import pipeline_bench
-    if not args.tp:  # PP 2/4 stages, PP4 x TP2 on the 8-GPU runs
+    if not args.tp:  # the headline layouts: PP 2/4 stages, PP4 x TP2 on the 8-GPU runs
         args.tp = 2 if args.gpus >= 8 else 1
     return pipeline_bench(args)
 

@@ -34,7 +34,7 @@
 // No TMA (and no multicast) touches peer memory: peers are only written with
 // plain stores, and the grouped GEMM reads its own arena through TMA.
 // Reference: the reference keeps every expert of a layer on the node holding
-// the layer (no expert parallelism; SURVEY of src/inference/layers/moe.rs);
+// the layer (no expert parallelism; src/inference/layers/moe.rs);
 // the closest behaviour is its network TP all-reduce (src/network/tp_*.rs).
 #include "kernels.h"
 #include "common.cuh"

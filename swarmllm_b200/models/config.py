@@ -145,7 +145,7 @@ def rope_inv_freq(cfg: ModelConfig) -> tuple[np.ndarray, float]:
 
 # --------------------------------------------------------------------------- presets
 def tiny_llama() -> ModelConfig:
-    """2 layers, hidden 256, 4/2 heads, d 64, FFN 512, Q4_0."""
+    """Tiny Llama for the two-CPU-peer split: 2 layers, hidden 256, 4/2 heads, d 64, FFN 512, Q4_0."""
     return ModelConfig(name="tiny-llama", arch="llama", n_layers=2, hidden=256, n_heads=4,
                        n_kv_heads=2, head_dim=64, ffn=512, vocab=32000, rope_theta=10000.0,
                        rms_eps=1e-5, weight_qtype="Q4_0", embed_qtype="Q4_0",
@@ -153,7 +153,7 @@ def tiny_llama() -> ModelConfig:
 
 
 def llama32_3b() -> ModelConfig:
-    """Llama-3.2-3B architecture, Q4_K weights."""
+    """Llama-3.2-3B architecture, Q4_K weights (single-GPU serving config)."""
     return ModelConfig(name="llama-3.2-3b", arch="llama", n_layers=28, hidden=3072, n_heads=24,
                        n_kv_heads=8, head_dim=128, ffn=8192, vocab=128256, rope_theta=500000.0,
                        rope_scaling={"type": "llama3", "factor": 32.0, "low_freq_factor": 1.0,
@@ -175,7 +175,7 @@ def llama32_1b() -> ModelConfig:
 
 
 def llama33_70b() -> ModelConfig:
-    """BASELINE config 3 / the headline: Llama-3.3-70B architecture, Q4_K."""
+    """Llama-3.3-70B architecture, Q4_K (the headline benchmark model)."""
     return ModelConfig(name="llama-3.3-70b", arch="llama", n_layers=80, hidden=8192, n_heads=64,
                        n_kv_heads=8, head_dim=128, ffn=28672, vocab=128256, rope_theta=500000.0,
                        rope_scaling={"type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
@@ -185,7 +185,7 @@ def llama33_70b() -> ModelConfig:
 
 
 def gpt_oss_120b_style() -> ModelConfig:
-    """gpt-oss-120B-style MoE (MXFP4 experts, bf16 attention)."""
+    """gpt-oss-120B-style MoE (MXFP4 experts, bf16 attention; expert-parallel config)."""
     return ModelConfig(name="gpt-oss-120b-style", arch="gpt-oss", n_layers=36, hidden=2880,
                        n_heads=64, n_kv_heads=8, head_dim=64, ffn=2880, vocab=201088,
                        rope_theta=150000.0, rope_neox=True,
@@ -199,7 +199,7 @@ def gpt_oss_120b_style() -> ModelConfig:
 
 
 def qwen3_next_80b_style() -> ModelConfig:
-    """Qwen3-Next-80B-A3B-style hybrid (3 DeltaNet : 1 gated attention)."""
+    """Qwen3-Next-80B-A3B-style hybrid (3 DeltaNet : 1 gated attention; long-prefill config)."""
     return ModelConfig(name="qwen3-next-80b-a3b-style", arch="qwen3next", n_layers=48,
                        hidden=2048, n_heads=16, n_kv_heads=2, head_dim=256, ffn=512,
                        vocab=151936, rope_theta=10000000.0, rope_neox=True, rope_dim=64,

@@ -469,7 +469,7 @@ def _has_simt(model: LlamaGPU) -> bool:
 # =========================================================================== CPU
 class LlamaCPU:
     """fp32 PyTorch implementation on the host: the oracle for the GPU path and
-    the engine backend for CPU-only runs."""
+    the engine backend for CPU-only runs (the two-CPU-peer tiny Llama)."""
 
     def __init__(self, cfg: ModelConfig, source, layer_range: tuple[int, int] | None = None,
                  kv_layer_offset: int | None = None, dtype=torch.float32):

@@ -17,7 +17,7 @@ src/network/protocol/layer_forward.rs:6), one request at a time.  Here:
   stage r works on micro-batch m while stage r+1 works on m-1;
 * the last stage selects tokens and sends them back to rank 0;
 * activations cross as the fp32 residual stream, so a split run is
-  bit-identical to a single-process run of the same batch.
+  bit-identical to a single-process run of the same batch (the two-CPU-peer tiny Llama setup).
 
 Stage boundaries come from the native planner (`plan_bottleneck`, uniform
 per-layer cost on one NVSwitch box).

@@ -1,4 +1,4 @@
-"""BASELINE config 1 (plumbing, no GPU): the tiny Llama (2 layers, hidden 256,
+"""Two-CPU-peer split (plumbing, no GPU): the tiny Llama (2 layers, hidden 256,
 4/2 heads, d 64, FFN 512, vocab 32000, Q4_0 weights, F32 norms) split layer 0 |
 layer 1 across 2 local processes over gloo; 4 prompts of 32 random ids,
 greedy decode of 64 tokens; logits must match a single-process run."""
