@@ -68,6 +68,9 @@ def main(argv=None):
         s.add_argument("--lora", action="append", default=[], metavar="NAME=PATH",
                        help="LoRA adapter GGUF; requests select it with model NAME")
         s.add_argument("--mmproj", default=None, help="image encoder GGUF (vision input)")
+        s.add_argument("--log-file", default=None, help="also log to this file (rotating, 50 MB x 3)")
+        s.add_argument("--log-json", action="store_true", help="log one JSON object per line")
+        s.add_argument("-v", "--verbose", action="count", default=0)
         if name == "serve":
             s.add_argument("--host", default="0.0.0.0")
             s.add_argument("--port", type=int, default=8800)
@@ -109,6 +112,8 @@ def main(argv=None):
         write_random_gguf(preset(args.model), args.out, args.seed)
         print(args.out)
         return
+    from .utils.logsetup import setup_logging
+    setup_logging(args.verbose, args.log_file, args.log_json)
     eng = _engine(args)
     if args.cmd == "info":
         print(json.dumps({"config": eng.cfg.to_dict(), "kv_pages": eng.bm.num_pages,

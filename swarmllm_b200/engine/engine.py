@@ -105,6 +105,7 @@ class LLMEngine:
         self.prompt_len: dict[int, int] = {}
         self._ids = itertools.count()
         self.profiler = StageProfiler()
+        model.profiler = self.profiler     # per-stage accounting inside the forward
         self.steps = 0
 
     # ------------------------------------------------------------------ construction

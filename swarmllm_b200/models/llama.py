@@ -349,26 +349,32 @@ class LlamaGPU:
         q = ctx.q[:N]
         ao = ctx.attn_out[:N]
         act = ctx.act[:N]
+        P = self._stage_ctx()
         for j, L in enumerate(self.layers):
             if L.linear:
-                self._deltanet(L, b, kv, ctx, x, N)
-                g = L.w_out(ctx.ssm_out[:N], ctx.gemm)
-                C().epi_residual_rmsnorm(g, h, None, L.ffn_norm, x, cfg.rms_eps)
+                with P("delta_rule"):
+                    self._deltanet(L, b, kv, ctx, x, N)
+                with P("o_proj+norm"):
+                    g = L.w_out(ctx.ssm_out[:N], ctx.gemm)
+                    C().epi_residual_rmsnorm(g, h, None, L.ffn_norm, x, cfg.rms_eps)
             else:
                 li = self.kv_off + L.kv_idx
-                g = self._lora(j, "qkv", x, L.wqkv(x, ctx.gemm), ctx, b)
-                gate = ctx.gate[:N] if L.gated else None
-                C().epi_rope_kv(g, L.qkv_bias, b.positions, b.slots, self.inv_freq, nq, nkv, d,
-                                cfg.rot_dim, cfg.rope_neox, self.attn_factor, q, kv.k(li),
-                                kv.v(li), kv.page_size, L.q_norm, L.k_norm, cfg.rms_eps, gate)
-                paged_attention(q, kv.k(li), kv.v(li), b.block_table, b.seq_lens, ctx.attn,
-                                ao.view(N, nq, d), b.max_len, self.scale, L.window, L.sinks,
-                                tree_mask=b.tree_mask, tree_start=b.tree_start,
-                                num_sms=ctx.gemm.num_sms, groups=b.groups)
-                if gate is not None:
-                    C().mul_f16(ao, gate)
-                g = self._lora(j, "o", ao, self._row_parallel(L.wo, ao, ctx), ctx, b)
-                C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
+                with P("qkv_proj+rope+kv_append"):
+                    g = self._lora(j, "qkv", x, L.wqkv(x, ctx.gemm), ctx, b)
+                    gate = ctx.gate[:N] if L.gated else None
+                    C().epi_rope_kv(g, L.qkv_bias, b.positions, b.slots, self.inv_freq, nq, nkv, d,
+                                    cfg.rot_dim, cfg.rope_neox, self.attn_factor, q, kv.k(li),
+                                    kv.v(li), kv.page_size, L.q_norm, L.k_norm, cfg.rms_eps, gate)
+                with P("attention"):
+                    paged_attention(q, kv.k(li), kv.v(li), b.block_table, b.seq_lens, ctx.attn,
+                                    ao.view(N, nq, d), b.max_len, self.scale, L.window, L.sinks,
+                                    tree_mask=b.tree_mask, tree_start=b.tree_start,
+                                    num_sms=ctx.gemm.num_sms, groups=b.groups)
+                    if gate is not None:
+                        C().mul_f16(ao, gate)
+                with P("o_proj+norm"):
+                    g = self._lora(j, "o", ao, self._row_parallel(L.wo, ao, ctx), ctx, b)
+                    C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
             if j + 1 < len(self.layers):
                 nxt_w, nxt_out = self.layers[j + 1].attn_norm, x
             elif self.last:
@@ -376,36 +382,63 @@ class LlamaGPU:
             else:
                 nxt_w, nxt_out = None, None
             if L.experts is not None:
-                # router logits live in the side workspace only until top-k
-                moe_route(x, L.router, L.router_b, ctx.moe, ctx.gemm_side,
-                          cfg.moe_softmax_after_topk)
-                sh = shg = None
-                if L.sh_gu is not None:
-                    S = cfg.shared_expert_ffn
-                    g = L.sh_gu(x, ctx.gemm)
-                    C().epi_swiglu(g, None, S, 0, False, 0.0, 0.0, ctx.act_sh[:N])
-                    shg = L.sh_gate(x, ctx.gemm_side)
-                    sh = L.sh_down(ctx.act_sh[:N], ctx.gemm)
-                if self.ep is not None:
-                    moe_experts_ep(x, L.experts, ctx.moe, self.ep, h, nxt_w, nxt_out, cfg.rms_eps,
-                                   sh, shg)
-                else:
-                    moe_experts(x, L.experts, ctx.moe, h, nxt_w, nxt_out, cfg.rms_eps, sh, shg)
+                with P("moe"):
+                    # router logits live in the side workspace only until top-k
+                    moe_route(x, L.router, L.router_b, ctx.moe, ctx.gemm_side,
+                              cfg.moe_softmax_after_topk)
+                    sh = shg = None
+                    if L.sh_gu is not None:
+                        S = cfg.shared_expert_ffn
+                        g = L.sh_gu(x, ctx.gemm)
+                        C().epi_swiglu(g, None, S, 0, False, 0.0, 0.0, ctx.act_sh[:N])
+                        shg = L.sh_gate(x, ctx.gemm_side)
+                        sh = L.sh_down(ctx.act_sh[:N], ctx.gemm)
+                    if self.ep is not None:
+                        moe_experts_ep(x, L.experts, ctx.moe, self.ep, h, nxt_w, nxt_out, cfg.rms_eps,
+                                       sh, shg)
+                    else:
+                        moe_experts(x, L.experts, ctx.moe, h, nxt_w, nxt_out, cfg.rms_eps, sh, shg)
                 continue
-            g = self._lora(j, "gu", x, L.wgu(x, ctx.gemm), ctx, b)
-            C().epi_swiglu(g, None, self.ffn_loc, 0, False, 0.0, 0.0, act)
-            g = self._lora(j, "down", act, self._row_parallel(L.wdown, act, ctx), ctx, b)
-            C().epi_residual_rmsnorm(g, h, None, nxt_w if nxt_w is not None else ctx.dummy_norm,
-                                     nxt_out, cfg.rms_eps)
+            with P("ffn_gate_up+act"):
+                g = self._lora(j, "gu", x, L.wgu(x, ctx.gemm), ctx, b)
+                C().epi_swiglu(g, None, self.ffn_loc, 0, False, 0.0, 0.0, act)
+            with P("ffn_down+norm"):
+                g = self._lora(j, "down", act, self._row_parallel(L.wdown, act, ctx), ctx, b)
+                C().epi_residual_rmsnorm(g, h, None, nxt_w if nxt_w is not None else ctx.dummy_norm,
+                                         nxt_out, cfg.rms_eps)
         if not self.last:
             return h
-        S = b.sample_rows.shape[0]
-        xs = ctx.xs[:S]
-        torch.index_select(x, 0, b.sample_rows, out=xs)
-        g = self.head(xs, ctx.gemm)
-        logits = ctx.logits[:S]
-        C().epi_copy(g, None, logits)
+        with P("lm_head"):
+            S = b.sample_rows.shape[0]
+            xs = ctx.xs[:S]
+            torch.index_select(x, 0, b.sample_rows, out=xs)
+            g = self.head(xs, ctx.gemm)
+            logits = ctx.logits[:S]
+            C().epi_copy(g, None, logits)
         return logits
+
+    def _stage_ctx(self):
+        """Stage context of the profiler (SWARMLLM_PROFILE=1), outside CUDA-graph
+        capture only; otherwise a no-op."""
+        prof = getattr(self, "profiler", None)
+        if prof is None or not prof.enabled or torch.cuda.is_current_stream_capturing():
+            return _NO_STAGE
+        return prof.stage
+
+
+class _NullStage:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+_NULL_STAGE = _NullStage()
+
+
+def _NO_STAGE(name: str):
+    return _NULL_STAGE
 
 
 class GpuForwardContext:

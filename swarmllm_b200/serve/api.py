@@ -41,10 +41,14 @@ from dataclasses import dataclass, field
 from fastapi import Request, WebSocket  # module level: route annotations resolve from globals
 
 from ..engine.sampling import SamplingParams
+from ..utils.logsetup import get_logger
 from ..utils.metrics import Metrics
 from .chat_template import render
 from .tools import (ToolSpec, content_prefix_len, format_tool_prompt, parse_tool_calls,
                     tool_choice_forbids, tools_from_anthropic, tools_from_openai)
+
+
+_log = get_logger("serve")
 
 
 @dataclass
@@ -115,6 +119,7 @@ class AsyncEngine:
                     self._subs[s.rid] = s
                     self.metrics.requests_started()
                 except Exception as e:  # bad request: report and drop
+                    _log.warning("request %d rejected: %s", s.rid, e)
                     s.loop.call_soon_threadsafe(s.q.put_nowait, ("error", str(e)))
             while True:
                 try:
@@ -143,6 +148,7 @@ class AsyncEngine:
                 outs = eng.step()
                 self.metrics.step(time.perf_counter() - t0, len(outs))
             except Exception as e:  # engine failure: fail every request in flight
+                _log.exception("engine step failed; %d requests failed", len(self._subs))
                 self.ready = False
                 for rid in list(self._subs):
                     s = self._subs.pop(rid)
