@@ -79,6 +79,9 @@ def main(argv=None):
             s.add_argument("--cors-origin", action="append", default=[],
                            help="extra browser origin allowed besides localhost")
             s.add_argument("--rpm", type=int, default=0, help="requests a minute per client (0: off)")
+            s.add_argument("--kv-persist", default=None,
+                           help="file to load the prefix KV cache from at start and save it to at exit "
+                                "(discarded when written by another build or model)")
             s.add_argument("--response-store", default=None,
                            help="SQLite file for stored /v1/responses (default: in memory)")
         if name == "generate":
@@ -112,7 +115,7 @@ def main(argv=None):
         write_random_gguf(preset(args.model), args.out, args.seed)
         print(args.out)
         return
-    from .utils.logsetup import setup_logging
+    from .utils.logsetup import get_logger, setup_logging
     setup_logging(args.verbose, args.log_file, args.log_json)
     eng = _engine(args)
     if args.cmd == "info":
@@ -122,10 +125,19 @@ def main(argv=None):
     if args.cmd == "serve":
         from .serve.api import serve
         tok, tpl = _tokenizer(args, eng)
-        serve(eng, tok, eng.cfg.name, args.host, args.port, arch=eng.cfg.arch, chat_template=tpl,
-              max_model_len=eng.ecfg.max_model_len, api_key=args.api_key,
-              cors_origins=tuple(args.cors_origin), rpm=args.rpm, store_path=args.response_store,
-              config_path=args.config)
+        log = get_logger("cli")
+        if args.kv_persist and eng.ecfg.prefix_cache:
+            log.info("prefix cache: %d tokens loaded from %s",
+                     eng.load_prefix_cache(args.kv_persist), args.kv_persist)
+        try:
+            serve(eng, tok, eng.cfg.name, args.host, args.port, arch=eng.cfg.arch,
+                  chat_template=tpl, max_model_len=eng.ecfg.max_model_len, api_key=args.api_key,
+                  cors_origins=tuple(args.cors_origin), rpm=args.rpm,
+                  store_path=args.response_store, config_path=args.config)
+        finally:
+            if args.kv_persist and eng.ecfg.prefix_cache:
+                log.info("prefix cache: %d tokens saved to %s",
+                         eng.save_prefix_cache(args.kv_persist), args.kv_persist)
         return
     from .engine.sampling import SamplingParams
     if args.cmd == "generate":

@@ -58,12 +58,15 @@ void BlockManager::release_page(int p) {
   }
 }
 
-int BlockManager::add_sequence(int64_t seq_id, const std::vector<int32_t>& tokens) {
+int BlockManager::add_sequence(int64_t seq_id, const std::vector<int32_t>& tokens,
+                               uint64_t salt) {
   if (seqs_.count(seq_id)) throw std::invalid_argument("sequence exists");
   Seq s;
+  s.root = salt;
+  s.last_hash = salt;
   int covered = 0;
   if (prefix_) {
-    uint64_t h = 0;
+    uint64_t h = salt;
     // Never map the whole prompt: the last token must be recomputed for logits.
     const int full = ((int)tokens.size() - 1) / page_size_;
     for (int i = 0; i < full; ++i) {
@@ -93,10 +96,11 @@ int BlockManager::add_sequence(int64_t seq_id, const std::vector<int32_t>& token
   return covered;
 }
 
-std::vector<int32_t> BlockManager::cached_prefix_pages(const std::vector<int32_t>& tokens) const {
+std::vector<int32_t> BlockManager::cached_prefix_pages(const std::vector<int32_t>& tokens,
+                                                       uint64_t salt) const {
   std::vector<int32_t> out;
   if (!prefix_) return out;
-  uint64_t h = 0;
+  uint64_t h = salt;
   const int full = (int)tokens.size() / page_size_;
   for (int i = 0; i < full; ++i) {
     const uint64_t nh = hash_page(h, tokens.data() + (size_t)i * page_size_, page_size_);
@@ -109,11 +113,11 @@ std::vector<int32_t> BlockManager::cached_prefix_pages(const std::vector<int32_t
 }
 
 std::vector<int32_t> BlockManager::import_prefix_pages(const std::vector<int32_t>& tokens,
-                                                       int n_pages) {
+                                                       int n_pages, uint64_t salt) {
   std::vector<int32_t> out;
   if (!prefix_) return out;
   n_pages = std::min(n_pages, (int)tokens.size() / page_size_);
-  uint64_t h = 0;
+  uint64_t h = salt;
   for (int i = 0; i < n_pages; ++i) {
     const uint64_t nh = hash_page(h, tokens.data() + (size_t)i * page_size_, page_size_);
     h = nh;
@@ -203,7 +207,7 @@ void BlockManager::truncate(int64_t seq_id, int new_len) {
   if (s.hashed_pages > s.len / page_size_) {
     // Recompute the hash chain up to the surviving full pages.
     s.hashed_pages = 0;
-    s.last_hash = 0;
+    s.last_hash = s.root;
     const int full = s.len / page_size_;
     for (int i = 0; i < full && i * page_size_ + page_size_ <= (int)s.tokens.size(); ++i) {
       s.last_hash = hash_page(s.last_hash, s.tokens.data() + (size_t)i * page_size_, page_size_);

@@ -28,7 +28,10 @@ class BlockManager {
 
   // Create a sequence.  With prefix caching, the longest run of full cached
   // pages matching `tokens` is mapped; returns the number of tokens covered.
-  int add_sequence(int64_t seq_id, const std::vector<int32_t>& tokens);
+  // `salt` is the root of the sequence's hash chain: sequences whose KV
+  // differs for the same tokens (another LoRA adapter) use another salt and
+  // never share pages.
+  int add_sequence(int64_t seq_id, const std::vector<int32_t>& tokens, uint64_t salt = 0);
   bool has_sequence(int64_t seq_id) const { return seqs_.count(seq_id) != 0; }
   int seq_len(int64_t seq_id) const;
   // Reserve room for n more tokens; returns the slot ids (page*page_size+off),
@@ -52,14 +55,16 @@ class BlockManager {
   // Prefix snapshots (export / import of cached KV pages, e.g. across nodes).
   // Pages of the longest cached chain of full pages of `tokens` (no
   // references are taken: copy them out before scheduling more work).
-  std::vector<int32_t> cached_prefix_pages(const std::vector<int32_t>& tokens) const;
+  std::vector<int32_t> cached_prefix_pages(const std::vector<int32_t>& tokens,
+                                           uint64_t salt = 0) const;
   // Make the first n_pages full pages of `tokens` cached: for each page of
   // the chain not already cached, take a free (or evict an LRU) page and
   // register its hash; it is left unreferenced in the LRU, as if a finished
   // request had produced it.  Returns one entry per page: the page to fill
   // with the KV data, or -1 where the page was already cached (or no page
   // was available; the chain stops there).
-  std::vector<int32_t> import_prefix_pages(const std::vector<int32_t>& tokens, int n_pages);
+  std::vector<int32_t> import_prefix_pages(const std::vector<int32_t>& tokens, int n_pages,
+                                           uint64_t salt = 0);
   int num_cached_pages() const { return (int)hash_to_page_.size(); }
 
  private:
@@ -69,6 +74,7 @@ class BlockManager {
     int len = 0;                  // reserved tokens
     int hashed_pages = 0;         // leading full pages already registered
     uint64_t last_hash = 0;
+    uint64_t root = 0;            // hash-chain root (salt)
   };
   int alloc_page();
   void release_page(int p);

@@ -28,7 +28,8 @@ PYBIND11_MODULE(_native, m) {
       .def_property_readonly("page_size", &BlockManager::page_size)
       .def_property_readonly("num_pages", &BlockManager::num_pages)
       .def("num_free", &BlockManager::num_free)
-      .def("add_sequence", &BlockManager::add_sequence)
+      .def("add_sequence", &BlockManager::add_sequence, py::arg("seq_id"), py::arg("tokens"),
+           py::arg("salt") = 0)
       .def("has_sequence", &BlockManager::has_sequence)
       .def("seq_len", &BlockManager::seq_len)
       .def("append_slots", [](BlockManager& b, int64_t id, int n) { return to_np(b.append_slots(id, n)); })
@@ -45,10 +46,13 @@ PYBIND11_MODULE(_native, m) {
              return a;
            })
       .def("cached_prefix_pages",
-           [](const BlockManager& b, const std::vector<int32_t>& t) { return to_np(b.cached_prefix_pages(t)); })
-      .def("import_prefix_pages", [](BlockManager& b, const std::vector<int32_t>& t, int n) {
-        return to_np(b.import_prefix_pages(t, n));
-      })
+           [](const BlockManager& b, const std::vector<int32_t>& t, uint64_t salt) {
+             return to_np(b.cached_prefix_pages(t, salt));
+           }, py::arg("tokens"), py::arg("salt") = 0)
+      .def("import_prefix_pages",
+           [](BlockManager& b, const std::vector<int32_t>& t, int n, uint64_t salt) {
+             return to_np(b.import_prefix_pages(t, n, salt));
+           }, py::arg("tokens"), py::arg("n_pages"), py::arg("salt") = 0)
       .def_property_readonly("prefix_hit_tokens", &BlockManager::prefix_hits)
       .def_property_readonly("num_cached_pages", &BlockManager::num_cached_pages);
 
@@ -70,7 +74,7 @@ PYBIND11_MODULE(_native, m) {
            py::arg("max_step_tokens"), py::arg("max_running"), py::arg("prefill_chunk"),
            py::keep_alive<1, 2>())
       .def("add_request", &Scheduler::add_request, py::arg("id"), py::arg("prompt"),
-           py::arg("max_new"), py::arg("eos") = -1)
+           py::arg("max_new"), py::arg("eos") = -1, py::arg("cache_salt") = 0)
       .def("abort", &Scheduler::abort)
       .def("schedule", &Scheduler::schedule)
       .def("commit", &Scheduler::commit)

@@ -12,7 +12,7 @@ Scheduler::Scheduler(BlockManager* bm, int max_step_tokens, int max_running, int
       prefill_chunk_(prefill_chunk) {}
 
 void Scheduler::add_request(int64_t id, const std::vector<int32_t>& prompt, int max_new,
-                            int32_t eos) {
+                            int32_t eos, uint64_t cache_salt) {
   if (reqs_.count(id)) throw std::invalid_argument("duplicate request id");
   if (prompt.empty()) throw std::invalid_argument("empty prompt");
   Request r;
@@ -20,6 +20,7 @@ void Scheduler::add_request(int64_t id, const std::vector<int32_t>& prompt, int 
   r.prompt = prompt;
   r.max_new = max_new;
   r.eos = eos;
+  r.cache_salt = cache_salt;
   r.arrival = clock_++;
   reqs_.emplace(id, std::move(r));
   waiting_.push_back(id);
@@ -108,7 +109,7 @@ StepPlan Scheduler::schedule() {
   while (!waiting_.empty() && budget > 0 && (int)running_.size() < max_running_) {
     const int64_t id = waiting_.front();
     Request& r = reqs_.at(id);
-    const int covered = bm_->add_sequence(id, r.prompt);
+    const int covered = bm_->add_sequence(id, r.prompt, r.cache_salt);
     r.n_computed = covered;
     const int remaining = (int)r.prompt.size() - covered;
     const int n = std::min({remaining, budget, prefill_chunk_});

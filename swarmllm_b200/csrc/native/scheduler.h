@@ -33,6 +33,7 @@ struct Request {
   bool finished = false;
   int64_t arrival = 0;
   int n_preempted = 0;
+  uint64_t cache_salt = 0;       // prefix-cache namespace (0: base model)
 };
 
 struct StepPlan {
@@ -51,7 +52,8 @@ struct StepPlan {
 class Scheduler {
  public:
   Scheduler(BlockManager* bm, int max_step_tokens, int max_running, int prefill_chunk);
-  void add_request(int64_t id, const std::vector<int32_t>& prompt, int max_new, int32_t eos);
+  void add_request(int64_t id, const std::vector<int32_t>& prompt, int max_new, int32_t eos,
+                   uint64_t cache_salt = 0);
   bool abort(int64_t id);
   StepPlan schedule();
   // Feed back the sampled token of each sequence with seq_sample == 1 (in batch

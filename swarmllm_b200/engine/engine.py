@@ -13,6 +13,8 @@ plus ModelProcessPool::generate (src/inference/process_pool.rs:14208).
 """
 from __future__ import annotations
 
+import collections
+import hashlib
 import itertools
 import time
 from dataclasses import dataclass, field
@@ -26,6 +28,18 @@ from ..utils.ext import native
 from ..utils.tracing import RequestTrace, StageProfiler
 from .runner import CpuRunner, GpuRunner
 from .sampling import SamplingParams
+
+
+RECENT_PROMPTS = 256   # released base-model prompts remembered for persisting the prefix cache
+
+
+def cache_salt(lora: str | None) -> int:
+    """Root of a request's prefix-cache hash chain: 0 for the base model, a
+    64-bit digest of the adapter name under a LoRA adapter, so the KV pages of
+    different adapters are never shared."""
+    if lora is None:
+        return 0
+    return int.from_bytes(hashlib.blake2b(lora.encode(), digest_size=8).digest(), "little") | 1
 
 
 @dataclass
@@ -103,6 +117,8 @@ class LLMEngine:
         self.params: dict[int, SamplingParams] = {}
         self.traces: dict[int, RequestTrace] = {}
         self.prompt_len: dict[int, int] = {}
+        self._prompts: dict[int, np.ndarray] = {}   # base-model prompts in flight
+        self._recent: collections.OrderedDict = collections.OrderedDict()  # released, LRU
         self._ids = itertools.count()
         self.profiler = StageProfiler()
         model.profiler = self.profiler     # per-stage accounting inside the forward
@@ -157,6 +173,21 @@ class LLMEngine:
         number of tokens newly cached."""
         from .prefix_share import import_prefix
         return import_prefix(self, snapshot)
+
+    def recent_prompts(self) -> list:
+        """Prompts of recently released requests, newest last (the candidates
+        for persisting the prefix cache)."""
+        return [p.tolist() for p in self._recent.values()]
+
+    def save_prefix_cache(self, path: str) -> int:
+        """Persist the cached prefixes of recent prompts (build-stamped file)."""
+        from .prefix_share import save_prefix_cache
+        return save_prefix_cache(self, path)
+
+    def load_prefix_cache(self, path: str) -> int:
+        """Load a file of save_prefix_cache; a file of another build is discarded."""
+        from .prefix_share import load_prefix_cache
+        return load_prefix_cache(self, path)
 
     def load_lora(self, adapter, name: str | None = None) -> str:
         """Register a LoRA adapter (a LoraAdapter or a LoRA GGUF path) for
@@ -213,7 +244,10 @@ class LLMEngine:
         if lora is not None:
             self.lora_of[rid] = self.lora_names.index(lora)
         eos = -1 if params.ignore_eos else params.eos_token_id
-        self.sched.add_request(rid, [int(t) for t in prompt_ids], int(params.max_tokens), int(eos))
+        self.sched.add_request(rid, [int(t) for t in prompt_ids], int(params.max_tokens), int(eos),
+                               cache_salt(lora))
+        if lora is None and self.ecfg.prefix_cache:
+            self._prompts[rid] = np.asarray(prompt_ids, dtype=np.int32)
         self.params[rid] = params
         self.prompt_len[rid] = len(prompt_ids)
         self.traces[rid] = RequestTrace(rid, len(prompt_ids))
@@ -223,6 +257,7 @@ class LLMEngine:
         self.sched.abort(rid)
         self._free_state(rid)
         self.images.pop(rid, None)
+        self._prompts.pop(rid, None)
 
     def _free_state(self, rid: int):
         slots = getattr(self.runner, "slots", None)
@@ -286,6 +321,13 @@ class LLMEngine:
         self.images.pop(rid, None)
         self.params.pop(rid, None)
         self.prompt_len.pop(rid, None)
+        p = self._prompts.pop(rid, None)
+        if p is not None and len(p) >= self.bm.page_size:
+            key = p.tobytes()
+            self._recent.pop(key, None)
+            self._recent[key] = p
+            while len(self._recent) > RECENT_PROMPTS:
+                self._recent.popitem(last=False)
 
     def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None
                  ) -> list[RequestOutput]:

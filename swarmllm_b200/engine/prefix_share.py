@@ -13,19 +13,30 @@ followed by the raw tensor, so it can go over any transport; `send_prefix` /
 Hybrid models (linear-attention state) keep no prefix cache, so they export
 nothing.
 
+`save_prefix_cache` / `load_prefix_cache` persist the whole cache across
+restarts: the snapshots of the engine's recent prompts in one file, stamped
+with a digest of the package version, the model (name, size, weight file) and
+the KV geometry.  A file whose stamp differs from the loading engine's is
+discarded, since its pages would not match the new weights or layout.
+
 Reference behaviour: KV snapshots keyed by block-hash chains and the
 PrefixKvFetchReq / PrefixKvDataResp exchange between peers
 (split/prefix_cache.rs:2359,2479; network/protocol/mod.rs:381-393).
 """
 from __future__ import annotations
 
+import hashlib
 import json
+import logging
+import os
 from dataclasses import dataclass
 
 import numpy as np
 import torch
 
 _MAGIC = b"SWKV1\0"
+_STORE_MAGIC = b"SWKVS1\0"
+_log = logging.getLogger("swarmllm_b200.prefix")
 _DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32}
 
 
@@ -119,3 +130,73 @@ def recv_prefix(src: int, group=None) -> PrefixSnapshot | None:
     buf = torch.empty(int(n), dtype=torch.uint8, device=dev)
     dist.recv(buf, src, group=group)
     return PrefixSnapshot.from_bytes(buf.cpu().numpy().tobytes())
+
+
+# --------------------------------------------------------------------------- persistence
+def build_stamp(engine) -> str:
+    """Digest of what the cached KV depends on: package version, model
+    identity (name, parameter count, weight file size and mtime) and the KV
+    cache geometry and dtype."""
+    from .. import __version__
+    src = getattr(engine, "source_path", None)
+    st = os.stat(src) if src and os.path.exists(src) else None
+    d = engine.kv.data
+    ident = {"v": __version__, "model": engine.cfg.name, "params": engine.cfg.param_count(),
+             "source": os.path.abspath(src) if src else None,
+             "size": st.st_size if st else None, "mtime": int(st.st_mtime) if st else None,
+             "page": engine.bm.page_size, "kv": [int(x) for x in d.shape[:1] + d.shape[3:]],
+             "dtype": str(d.dtype)}
+    return hashlib.sha256(json.dumps(ident, sort_keys=True).encode()).hexdigest()[:32]
+
+
+def _covering(prompts) -> list:
+    """Drop prompts that are a prefix of another one (their pages are inside it)."""
+    ps = sorted((tuple(int(x) for x in p) for p in prompts), key=len, reverse=True)
+    out: list = []
+    for p in ps:
+        if not any(q[: len(p)] == p for q in out):
+            out.append(p)
+    return out
+
+
+def save_prefix_cache(engine, path: str) -> int:
+    """Write the cached prefixes of the engine's recent prompts to `path`
+    (atomically); returns the number of tokens saved."""
+    snaps = []
+    for p in _covering(engine.recent_prompts()):
+        s = export_prefix(engine, list(p))
+        if s is not None:
+            snaps.append(s.to_bytes())
+    head = json.dumps({"stamp": build_stamp(engine), "sizes": [len(b) for b in snaps]}).encode()
+    tmp = f"{path}.tmp"
+    with open(tmp, "wb") as f:
+        f.write(_STORE_MAGIC + len(head).to_bytes(8, "little") + head)
+        for b in snaps:
+            f.write(b)
+    os.replace(tmp, path)
+    return sum(PrefixSnapshot.from_bytes(b).n_pages for b in snaps) * engine.bm.page_size
+
+
+def load_prefix_cache(engine, path: str) -> int:
+    """Import a file written by save_prefix_cache; returns the tokens newly
+    cached.  A missing file, a file of another build or model (stamp
+    mismatch) or an unreadable one loads nothing."""
+    if not os.path.exists(path):
+        return 0
+    with open(path, "rb") as f:
+        b = f.read()
+    if not b.startswith(_STORE_MAGIC):
+        _log.warning("%s is not a prefix-cache file; ignored", path)
+        return 0
+    o = len(_STORE_MAGIC)
+    n = int.from_bytes(b[o:o + 8], "little")
+    head = json.loads(b[o + 8:o + 8 + n].decode())
+    if head.get("stamp") != build_stamp(engine):
+        _log.warning("%s was written by another build or model; discarded", path)
+        return 0
+    o += 8 + n
+    total = 0
+    for sz in head["sizes"]:
+        total += import_prefix(engine, PrefixSnapshot.from_bytes(b[o:o + sz]))
+        o += sz
+    return total

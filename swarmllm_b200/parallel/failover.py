@@ -24,6 +24,9 @@ Reference behaviour: HealthMonitor pings and missed-ping death
 (src/health/monitor.rs:702-704,904), router retry with re-planning
 (src/inference/router/mod.rs:524,598,659), failover_segment onto standbys and
 replay of retained activations (src/inference/pipeline/distributed.rs:2461).
+
+Ranks that fail repeatedly (missing at a recovery, or stale while alive) are
+ejected for a while by an OutlierTracker and left out of the membership.
 """
 from __future__ import annotations
 
@@ -48,10 +51,45 @@ class RankFailure(RuntimeError):
     pass
 
 
+class OutlierTracker:
+    """Failure counts per rank over a sliding window.  A rank with `limit`
+    failures inside `window_s` is ejected for `eject_s`: the root leaves it
+    out of the next memberships even if it registers as alive (a straggler
+    whose heartbeat keeps going stale, a rank that keeps breaking the group).
+    Reference behaviour: peers that keep failing a model are left out for a
+    while (src/daemon/state/peer_outliers.rs:60-106)."""
+
+    def __init__(self, limit: int = 2, window_s: float = 600.0, eject_s: float = 1800.0,
+                 clock=time.monotonic):
+        self.limit, self.window_s, self.eject_s, self.clock = limit, window_s, eject_s, clock
+        self._fails: dict[int, list[float]] = {}
+        self._until: dict[int, float] = {}
+
+    def record(self, rank: int):
+        now = self.clock()
+        f = [t for t in self._fails.get(rank, []) if now - t <= self.window_s] + [now]
+        self._fails[rank] = f
+        if len(f) >= self.limit:
+            self._until[rank] = now + self.eject_s
+            self._fails[rank] = []
+
+    def ejected(self) -> set[int]:
+        now = self.clock()
+        for r in [r for r, t in self._until.items() if t <= now]:
+            del self._until[r]
+        return set(self._until)
+
+    def members(self, alive: list[int]) -> list[int]:
+        """The next membership: alive ranks minus the ejected ones (never
+        empty: the ranks asking are alive, so the first of them stays)."""
+        out = [r for r in alive if r not in self.ejected()]
+        return out or alive[:1]
+
+
 class ResilientPipeline:
     def __init__(self, build_engine, rank: int, world: int, ctl_host: str, ctl_port: int,
                  backend: str = "gloo", pg_timeout_s: float = 10.0, grace_s: float | None = None,
-                 heartbeat_stale_s: float = 30.0):
+                 heartbeat_stale_s: float = 30.0, outliers: OutlierTracker | None = None):
         """`build_engine()` returns a PipelineEngine over the current default
         process group; it is called again after every re-plan."""
         self.rank, self.world0 = rank, world
@@ -66,6 +104,8 @@ class ResilientPipeline:
         self.epoch = 0
         self.build_engine = build_engine
         self.recoveries = 0
+        self.outliers = outliers or OutlierTracker()
+        self._suspects: list[int] = []     # stale ranks seen by the root before a recovery
         self._form_group()
         self.eng = build_engine()
 
@@ -110,7 +150,11 @@ class ResilientPipeline:
             time.sleep(self.grace_s)
             alive = [r for r in self.members
                      if self.store.check([f"alive/{self.epoch}/{r}"])]
-            self.store.set(key, ",".join(map(str, alive)))
+            for r in self.members:
+                if r not in alive or r in self._suspects:
+                    self.outliers.record(r)
+            self._suspects = []
+            self.store.set(key, ",".join(map(str, self.outliers.members(alive))))
         self.store.wait([key], datetime.timedelta(seconds=60))
         self.members = [int(x) for x in self.store.get(key).decode().split(",")]
         if self.rank not in self.members:
@@ -143,8 +187,11 @@ class ResilientPipeline:
                         r.done = r.done or fin
                     step += 1
                     self._heartbeat(step)
-                    if self.root and self.stale_ranks():
-                        raise RankFailure(f"stale heartbeat: {self.stale_ranks()}")
+                    if self.root:
+                        stale = self.stale_ranks()
+                        if stale:
+                            self._suspects = stale
+                            raise RankFailure(f"stale heartbeat: {stale}")
                 return [r.out for r in reqs] if self.root else None
             except (RuntimeError, dist.DistBackendError):
                 if self.recoveries >= max_recoveries:

@@ -31,6 +31,7 @@ from __future__ import annotations
 
 import asyncio
 import itertools
+import os
 import json
 import queue
 import threading
@@ -63,9 +64,23 @@ class _Sub:
 
 
 class AsyncEngine:
-    def __init__(self, engine, metrics: Metrics | None = None):
+    """The engine on its own thread; HTTP handlers talk to it through queues.
+
+    Readiness (`ready`) is withdrawn when a step raised, when the thread died,
+    or while the loop is stalled: one step running, or submitted work left
+    untouched, for more than `stall_s` seconds (default 300, env
+    SWARMLLM_STALL_S).  A stall that ends gives readiness back.
+    Reference behaviour: a dispatcher silent for 300 s withdraws the node's
+    inference capability (docs/ARCHITECTURE.md:354-377)."""
+
+    def __init__(self, engine, metrics: Metrics | None = None, stall_s: float | None = None):
         self.engine = engine
         self.metrics = metrics or Metrics()
+        self.stall_s = float(os.environ.get("SWARMLLM_STALL_S", "300")) if stall_s is None else stall_s
+        self._failed = False
+        self._beat = time.monotonic()          # last pass of the loop
+        self._step_since: float | None = None  # start of the step in progress
+        self._stall_logged = False
         self._in: queue.Queue = queue.Queue()
         self._abort: queue.Queue = queue.Queue()
         self._calls: queue.Queue = queue.Queue()
@@ -73,7 +88,6 @@ class AsyncEngine:
         self._ids = itertools.count(1)
         self._wake = threading.Event()
         self._stop = False
-        self.ready = True
         self._t = threading.Thread(target=self._run, daemon=True, name="engine")
         self._t.start()
 
@@ -98,6 +112,25 @@ class AsyncEngine:
         self._wake.set()
         return await fut
 
+    def stalled(self) -> bool:
+        now = time.monotonic()
+        if self._step_since is not None and now - self._step_since > self.stall_s:
+            return True
+        return not self._in.empty() and now - self._beat > self.stall_s
+
+    @property
+    def ready(self) -> bool:
+        if self._failed or not self._t.is_alive():
+            return False
+        st = self.stalled()
+        if st != self._stall_logged:
+            self._stall_logged = st
+            if st:
+                _log.error("engine loop stalled for more than %.0f s: not ready", self.stall_s)
+            else:
+                _log.warning("engine loop resumed")
+        return not st
+
     def shutdown(self):
         self._stop = True
         self._wake.set()
@@ -106,6 +139,7 @@ class AsyncEngine:
     def _run(self):
         eng = self.engine
         while not self._stop:
+            self._beat = time.monotonic()
             while True:
                 try:
                     s = self._in.get_nowait()
@@ -145,11 +179,15 @@ class AsyncEngine:
                 continue
             try:
                 t0 = time.perf_counter()
-                outs = eng.step()
+                self._step_since = time.monotonic()
+                try:
+                    outs = eng.step()
+                finally:
+                    self._step_since = None
                 self.metrics.step(time.perf_counter() - t0, len(outs))
             except Exception as e:  # engine failure: fail every request in flight
                 _log.exception("engine step failed; %d requests failed", len(self._subs))
-                self.ready = False
+                self._failed = True
                 for rid in list(self._subs):
                     s = self._subs.pop(rid)
                     s.loop.call_soon_threadsafe(s.q.put_nowait, ("error", repr(e)))

@@ -1,10 +1,11 @@
 """Standalone cases of the hot kernels, for profiling one kernel at a time:
 
-    python -m swarmllm_b200.utils.kernel_cases {qgemm|qgemv|qgemv_o|dense|attn|moe|delta}
+    python -m swarmllm_b200.utils.kernel_cases \
+        {qgemm|qgemv|qgemv_o|dense|attn|attn_prefill|rmsnorm|swiglu|moe|delta|tree_rank|sample}
 
 Each case builds benchmark-sized operands on cuda:0 (inputs larger than the
-126 MB L2 where memory traffic matters), runs the kernel a few times and
-exits.  Under ncu, capture one launch after the warm-up ones, e.g.
+126 MB L2 where memory traffic matters; tree_rank and sample use the real
+logits size, which L2 holds), runs the kernel a few times and exits.  Under ncu, capture one launch after the warm-up ones, e.g.
 
     ncu --set full --clock-control none -k regex:qgemm_q4k -s 2 -c 1 \
         -o prof_qgemm python -m swarmllm_b200.utils.kernel_cases qgemm
@@ -64,6 +65,60 @@ elif which == "attn":      # decode batch 32, context 2300, 64 q / 8 kv heads, d
     out = torch.empty_like(q)
     for _ in range(5):
         paged_attention(q, K, V, bt, lens, ws, out, L + 64, 1 / math.sqrt(d))
+elif which == "attn_prefill":  # 70B prefill chunk: 2048 causal positions of one sequence
+    from swarmllm_b200.ops.attention import AttentionWorkspace, paged_attention
+    T, nq, nkv, d, ps = 2048, 64, 8, 128, 16
+    P = T // ps
+    K = torch.randn(P, nkv, ps, d, device=dev).half(); V = torch.randn_like(K)
+    bt = torch.arange(P, device=dev, dtype=torch.int32).view(1, P).expand(T, P).contiguous()
+    lens = torch.arange(1, T + 1, dtype=torch.int32, device=dev)
+    ppg = 128 // (nq // nkv)      # positions per row group
+    row0 = torch.arange(0, T, ppg, dtype=torch.int32, device=dev)
+    npos = torch.full_like(row0, ppg)
+    q = torch.randn(T, nq, d, device=dev).half()
+    ws = AttentionWorkspace(dev, T, nq, nkv, d, T)
+    out = torch.empty_like(q)
+    for _ in range(5):
+        paged_attention(q, K, V, bt, lens, ws, out, T, 1 / math.sqrt(d), groups=(row0, npos, ppg))
+elif which == "rmsnorm":   # down projection + residual-add/RMSNorm epilogue, 2048-token chunk
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    rows, K, T = 8192, 28672, 2048
+    lin = QLinear(rand_q4k(rows, K), Q.Q4_K, rows, K, dev)
+    ws = GemmWorkspace(dev, T, rows)
+    x = torch.randn(T, K, device=dev).half()
+    h = torch.randn(T, rows, device=dev)
+    w = torch.ones(rows, device=dev)
+    out = torch.empty(T, rows, device=dev).half()
+    for _ in range(5):
+        C().epi_residual_rmsnorm(lin(x, ws), h, None, w, out, 1e-5)
+elif which == "swiglu":    # gate|up projection + SwiGLU epilogue, 2048-token chunk
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    rows, K, T = 57344, 8192, 2048
+    lin = QLinear(rand_q4k(rows, K), Q.Q4_K, rows, K, dev)
+    ws = GemmWorkspace(dev, T, rows)
+    x = torch.randn(T, K, device=dev).half()
+    act = torch.empty(T, rows // 2, device=dev).half()
+    for _ in range(5):
+        C().epi_swiglu(lin(x, ws), None, rows // 2, 0, False, 0.0, 0.0, act)
+elif which == "tree_rank":  # drafter top-4 over a 128256 vocabulary, 32 sequences x width 4
+    rows, V, W = 128, 128256, 4
+    logits = torch.randn(rows, V, device=dev) * 3
+    ids = torch.zeros(rows * W, dtype=torch.int32, device=dev)
+    lp = torch.zeros(rows * W, device=dev)
+    rk = torch.zeros(int(C().tree_rank_ws_floats(rows, V, W)), device=dev)
+    for _ in range(5):
+        C().tree_rank(logits, W, ids, lp, rk)
+elif which == "sample":     # temperature / top-k / top-p sampling of 32 rows over 128256 tokens
+    rows, V = 32, 128256
+    logits = torch.randn(rows, V, device=dev) * 3
+    temp = torch.full((rows,), 0.8, device=dev)
+    topk = torch.full((rows,), 40, dtype=torch.int32, device=dev)
+    topp = torch.full((rows,), 0.95, device=dev)
+    seeds = torch.arange(rows, dtype=torch.int64, device=dev)
+    pos = torch.full((rows,), 100, dtype=torch.int32, device=dev)
+    out = torch.zeros(rows, dtype=torch.int32, device=dev)
+    for _ in range(5):
+        C().sample(logits, temp, topk, topp, seeds, pos, out)
 elif which == "moe":       # gpt-oss-style experts (32 of 128, MXFP4), batch 64 tokens top-4
     from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
     from swarmllm_b200.ops.moe import MoeExperts, MoeWorkspace, moe_ffn

@@ -393,3 +393,38 @@ def test_admin_api(tmp_path):
         assert d["native_extensions"]["swarmllm_b200._native"] and d["kv_cache"]["pages"] > 0
         assert c.get("/api/admin/responses", headers=h).json()["data"] == []
     ae.shutdown()
+
+
+def test_stalled_engine_withdraws_readiness():
+    """A step that does not return for longer than stall_s takes /health/ready
+    to 503; readiness comes back when the step returns."""
+    import threading
+
+    from fastapi.testclient import TestClient
+
+    from swarmllm_b200.serve.api import AsyncEngine, create_app
+    from swarmllm_b200.serve.tokenizer import ByteTokenizer
+    gate = threading.Event()
+
+    class Blocking(Scripted):
+        def step(self):
+            gate.wait(5.0)
+            return super().step()
+
+    eng = Blocking("ab")
+    ae = AsyncEngine(eng, stall_s=0.2)
+    app = create_app(ae, ByteTokenizer(512), "m", max_model_len=4096)
+    with TestClient(app) as c:
+        assert c.get("/health/ready").status_code == 200
+        eng.add_request([5], types.SimpleNamespace(max_tokens=2), request_id=99)
+        ae._wake.set()
+        t0 = time.time()
+        while c.get("/health/ready").status_code != 503:
+            assert time.time() - t0 < 3, "stall not detected"
+            time.sleep(0.05)
+        assert ae.stalled() and c.get("/api/status").json()["ready"] is False
+        gate.set()
+        while c.get("/health/ready").status_code != 200:
+            assert time.time() - t0 < 6, "readiness did not come back"
+            time.sleep(0.05)
+    ae.shutdown()

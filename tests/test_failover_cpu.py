@@ -91,3 +91,22 @@ def test_stage_failure_replans_and_replays():
     assert procs[0].exitcode == 0 and procs[1].exitcode == 0
     assert recoveries == 1 and members == [0, 1]
     assert out == want
+
+
+def test_outlier_tracker_ejects_repeat_failures():
+    from swarmllm_b200.parallel.failover import OutlierTracker
+    now = [0.0]
+    t = OutlierTracker(limit=2, window_s=10.0, eject_s=100.0, clock=lambda: now[0])
+    t.record(3)
+    assert t.ejected() == set() and t.members([0, 1, 3]) == [0, 1, 3]
+    now[0] = 20.0                       # the first failure left the window
+    t.record(3)
+    assert t.ejected() == set()
+    now[0] = 25.0
+    t.record(3)                         # two inside the window: ejected
+    assert t.ejected() == {3} and t.members([0, 1, 3]) == [0, 1]
+    now[0] = 126.0                      # cool-down over
+    assert t.ejected() == set() and t.members([0, 1, 3]) == [0, 1, 3]
+    t2 = OutlierTracker(limit=1, clock=lambda: now[0])
+    t2.record(0)
+    assert t2.members([0]) == [0]       # never an empty membership

@@ -126,3 +126,37 @@ def test_export_import_gpu_engine():
     hits0 = b.bm.prefix_hit_tokens
     assert _gen(b, PROMPT) == out_a
     assert b.bm.prefix_hit_tokens - hits0 == 64
+
+
+def test_persisted_cache_reloads_and_stamp_mismatch_discards(tmp_path):
+    a = _engine()
+    out_a = _gen(a, PROMPT)
+    _gen(a, PROMPT[:40])                       # a prefix of the first: saved inside it
+    path = str(tmp_path / "kv.bin")
+    assert a.save_prefix_cache(path) == 64
+    b = _engine()
+    assert b.load_prefix_cache(path) == 64
+    hits0 = b.bm.prefix_hit_tokens
+    assert _gen(b, PROMPT) == out_a
+    assert b.bm.prefix_hit_tokens - hits0 == 64
+    c = _engine()
+    c.cfg.name = "another-model"               # another model: the stamp differs
+    assert c.load_prefix_cache(path) == 0 and c.bm.num_cached_pages == 0
+    assert _engine().load_prefix_cache(str(tmp_path / "missing.bin")) == 0
+
+
+def test_cache_salt_separates_namespaces():
+    from swarmllm_b200.engine.engine import cache_salt
+    from swarmllm_b200.utils.ext import native
+    N = native()
+    bm = N.BlockManager(64, 16, True)
+    toks = list(range(100, 150))
+    assert bm.add_sequence(1, toks) == 0
+    bm.append_slots(1, len(toks))
+    bm.commit_tokens(1, toks)
+    bm.free_sequence(1)
+    s = cache_salt("adapter-a")
+    assert s != 0 and s != cache_salt("adapter-b") and cache_salt(None) == 0
+    assert bm.add_sequence(2, toks, s) == 0           # other namespace: no hit
+    assert bm.add_sequence(3, toks) == 48              # base namespace: 3 pages hit
+    assert len(bm.cached_prefix_pages(toks)) == 3 and len(bm.cached_prefix_pages(toks, s)) == 0
