@@ -58,8 +58,20 @@ void BlockManager::release_page(int p) {
   }
 }
 
+std::vector<uint64_t> BlockManager::chain_hashes(const std::vector<int32_t>& tokens, int n_pages,
+                                                 uint64_t salt) const {
+  std::vector<uint64_t> out;
+  n_pages = std::min(n_pages, (int)tokens.size() / page_size_);
+  uint64_t h = salt;
+  for (int i = 0; i < n_pages; ++i) {
+    h = hash_page(h, tokens.data() + (size_t)i * page_size_, page_size_);
+    out.push_back(h);
+  }
+  return out;
+}
+
 int BlockManager::add_sequence(int64_t seq_id, const std::vector<int32_t>& tokens,
-                               uint64_t salt) {
+                               uint64_t salt, int cap, bool exact) {
   if (seqs_.count(seq_id)) throw std::invalid_argument("sequence exists");
   Seq s;
   s.root = salt;
@@ -68,7 +80,8 @@ int BlockManager::add_sequence(int64_t seq_id, const std::vector<int32_t>& token
   if (prefix_) {
     uint64_t h = salt;
     // Never map the whole prompt: the last token must be recomputed for logits.
-    const int full = ((int)tokens.size() - 1) / page_size_;
+    int full = ((int)tokens.size() - 1) / page_size_;
+    if (cap >= 0) full = std::min(full, cap / page_size_);
     for (int i = 0; i < full; ++i) {
       uint64_t nh = hash_page(h, tokens.data() + (size_t)i * page_size_, page_size_);
       auto it = hash_to_page_.find(nh);
@@ -85,6 +98,12 @@ int BlockManager::add_sequence(int64_t seq_id, const std::vector<int32_t>& token
       s.pages.push_back(p);
       h = nh;
       covered += page_size_;
+    }
+    if (exact && cap >= 0 && covered != (cap / page_size_) * page_size_) {
+      for (int p : s.pages) release_page(p);   // back to the LRU / free list
+      s.pages.clear();
+      h = salt;
+      covered = 0;
     }
     s.hashed_pages = (int)s.pages.size();
     s.last_hash = h;

@@ -30,8 +30,14 @@ class BlockManager {
   // pages matching `tokens` is mapped; returns the number of tokens covered.
   // `salt` is the root of the sequence's hash chain: sequences whose KV
   // differs for the same tokens (another LoRA adapter) use another salt and
-  // never share pages.
-  int add_sequence(int64_t seq_id, const std::vector<int32_t>& tokens, uint64_t salt = 0);
+  // never share pages.  At most `cap` tokens are mapped (< 0: no cap); with
+  // `exact`, a hit shorter than `cap` maps nothing (a sequence that can only
+  // resume at one position: recurrent state saved there).
+  int add_sequence(int64_t seq_id, const std::vector<int32_t>& tokens, uint64_t salt = 0,
+                   int cap = -1, bool exact = false);
+  // Chained hash of each leading full page of `tokens` (the prefix-cache keys).
+  std::vector<uint64_t> chain_hashes(const std::vector<int32_t>& tokens, int n_pages,
+                                     uint64_t salt = 0) const;
   bool has_sequence(int64_t seq_id) const { return seqs_.count(seq_id) != 0; }
   int seq_len(int64_t seq_id) const;
   // Reserve room for n more tokens; returns the slot ids (page*page_size+off),

@@ -29,6 +29,8 @@ PYBIND11_MODULE(_native, m) {
       .def_property_readonly("num_pages", &BlockManager::num_pages)
       .def("num_free", &BlockManager::num_free)
       .def("add_sequence", &BlockManager::add_sequence, py::arg("seq_id"), py::arg("tokens"),
+           py::arg("salt") = 0, py::arg("cap") = -1, py::arg("exact") = false)
+      .def("chain_hashes", &BlockManager::chain_hashes, py::arg("tokens"), py::arg("n_pages"),
            py::arg("salt") = 0)
       .def("has_sequence", &BlockManager::has_sequence)
       .def("seq_len", &BlockManager::seq_len)
@@ -74,7 +76,8 @@ PYBIND11_MODULE(_native, m) {
            py::arg("max_step_tokens"), py::arg("max_running"), py::arg("prefill_chunk"),
            py::keep_alive<1, 2>())
       .def("add_request", &Scheduler::add_request, py::arg("id"), py::arg("prompt"),
-           py::arg("max_new"), py::arg("eos") = -1, py::arg("cache_salt") = 0)
+           py::arg("max_new"), py::arg("eos") = -1, py::arg("cache_salt") = 0,
+           py::arg("max_cover") = -1, py::arg("cover_exact") = false, py::arg("split_at") = -1)
       .def("abort", &Scheduler::abort)
       .def("schedule", &Scheduler::schedule)
       .def("commit", &Scheduler::commit)

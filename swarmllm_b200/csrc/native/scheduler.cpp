@@ -12,7 +12,8 @@ Scheduler::Scheduler(BlockManager* bm, int max_step_tokens, int max_running, int
       prefill_chunk_(prefill_chunk) {}
 
 void Scheduler::add_request(int64_t id, const std::vector<int32_t>& prompt, int max_new,
-                            int32_t eos, uint64_t cache_salt) {
+                            int32_t eos, uint64_t cache_salt, int max_cover, bool cover_exact,
+                            int split_at) {
   if (reqs_.count(id)) throw std::invalid_argument("duplicate request id");
   if (prompt.empty()) throw std::invalid_argument("empty prompt");
   Request r;
@@ -21,6 +22,9 @@ void Scheduler::add_request(int64_t id, const std::vector<int32_t>& prompt, int 
   r.max_new = max_new;
   r.eos = eos;
   r.cache_salt = cache_salt;
+  r.max_cover = max_cover;
+  r.cover_exact = cover_exact;
+  r.split_at = split_at;
   r.arrival = clock_++;
   reqs_.emplace(id, std::move(r));
   waiting_.push_back(id);
@@ -54,6 +58,10 @@ void Scheduler::preempt(int64_t id) {
 StepPlan Scheduler::schedule() {
   StepPlan plan;
   int budget = max_step_tokens_;
+  // A prefill chunk stops at the request's split position.
+  auto clip = [&](const Request& r, int n) {
+    return (r.split_at > r.n_computed && r.n_computed + n > r.split_at) ? r.split_at - r.n_computed : n;
+  };
   auto emit = [&](int64_t id, int ntok, bool sample, bool decode) {
     Request& r = reqs_.at(id);
     std::vector<int32_t> slots = bm_->append_slots(id, ntok);
@@ -101,7 +109,7 @@ StepPlan Scheduler::schedule() {
     Request& r = reqs_.at(id);
     const int remaining = (int)r.prompt.size() - r.n_computed;
     if (remaining <= 0) continue;
-    const int n = std::min({remaining, budget, prefill_chunk_});
+    const int n = clip(r, std::min({remaining, budget, prefill_chunk_}));
     if (!bm_->can_append({id}, n)) continue;
     if (emit(id, n, n == remaining, false)) budget -= n;
   }
@@ -109,16 +117,19 @@ StepPlan Scheduler::schedule() {
   while (!waiting_.empty() && budget > 0 && (int)running_.size() < max_running_) {
     const int64_t id = waiting_.front();
     Request& r = reqs_.at(id);
-    const int covered = bm_->add_sequence(id, r.prompt, r.cache_salt);
+    const int covered = bm_->add_sequence(id, r.prompt, r.cache_salt, r.max_cover, r.cover_exact);
     r.n_computed = covered;
     const int remaining = (int)r.prompt.size() - covered;
-    const int n = std::min({remaining, budget, prefill_chunk_});
+    const int n = clip(r, std::min({remaining, budget, prefill_chunk_}));
     if (!bm_->can_append({id}, n)) {
       bm_->free_sequence(id);
       r.n_computed = 0;
       break;
     }
     waiting_.pop_front();
+    // A request re-admitted after preemption recomputes from the start when
+    // its hit had to be exact (the saved state belongs to the first admission).
+    if (r.cover_exact) r.max_cover = 0;
     r.running = true;
     running_.push_back(id);
     if (emit(id, n, n == remaining, false)) budget -= n;

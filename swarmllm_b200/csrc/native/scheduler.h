@@ -34,6 +34,9 @@ struct Request {
   int64_t arrival = 0;
   int n_preempted = 0;
   uint64_t cache_salt = 0;       // prefix-cache namespace (0: base model)
+  int max_cover = -1;            // prefix-cache hit cap at first admission (< 0: none)
+  bool cover_exact = false;      // hit exactly max_cover tokens or none
+  int split_at = -1;             // a prefill chunk ends at this position (state snapshot)
 };
 
 struct StepPlan {
@@ -53,7 +56,8 @@ class Scheduler {
  public:
   Scheduler(BlockManager* bm, int max_step_tokens, int max_running, int prefill_chunk);
   void add_request(int64_t id, const std::vector<int32_t>& prompt, int max_new, int32_t eos,
-                   uint64_t cache_salt = 0);
+                   uint64_t cache_salt = 0, int max_cover = -1, bool cover_exact = false,
+                   int split_at = -1);
   bool abort(int64_t id);
   StepPlan schedule();
   // Feed back the sampled token of each sequence with seq_sample == 1 (in batch

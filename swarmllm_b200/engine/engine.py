@@ -55,6 +55,7 @@ class EngineConfig:
     cuda_graphs: bool = True
     graph_sizes: tuple = (1, 2, 4, 8, 16, 32, 64)
     max_loras: int = 0              # LoRA adapter slots (0: LoRA off)
+    state_cache_entries: int = 8    # hybrid models: saved recurrent states for prefix hits
     max_lora_rank: int = 64
 
 
@@ -75,8 +76,8 @@ class LLMEngine:
         N = native()
         ps = ecfg.page_size
         lin = model.linear_state_spec() if hasattr(model, "linear_state_spec") else None
-        if lin is not None:
-            # recurrent state cannot be rebuilt from cached KV pages
+        if lin is not None and ecfg.state_cache_entries <= 0:
+            # recurrent state cannot be rebuilt from cached KV pages alone
             ecfg.prefix_cache = False
         n_kv_layers = getattr(model, "n_kv_layers", model.hi - model.lo)
         self.lora_of: dict[int, int] = {}
@@ -114,6 +115,11 @@ class LLMEngine:
             self.runner.lora_of = self.lora_of if ecfg.max_loras else None
             self.runner.images = self.images
         self.sched = N.Scheduler(self.bm, ecfg.max_step_tokens, ecfg.max_running, ecfg.prefill_chunk)
+        self.state_cache = None
+        self._hyb: dict[int, dict] = {}     # hybrid requests: pending state restore / save
+        if lin is not None and ecfg.prefix_cache:
+            from .state_cache import StateCache
+            self.state_cache = StateCache(self.kv, ecfg.state_cache_entries)
         self.params: dict[int, SamplingParams] = {}
         self.traces: dict[int, RequestTrace] = {}
         self.prompt_len: dict[int, int] = {}
@@ -244,8 +250,12 @@ class LLMEngine:
         if lora is not None:
             self.lora_of[rid] = self.lora_names.index(lora)
         eos = -1 if params.ignore_eos else params.eos_token_id
-        self.sched.add_request(rid, [int(t) for t in prompt_ids], int(params.max_tokens), int(eos),
-                               cache_salt(lora))
+        salt = cache_salt(lora)
+        if self.state_cache is not None:
+            self._add_hybrid(rid, prompt_ids, params, eos, salt)
+        else:
+            self.sched.add_request(rid, [int(t) for t in prompt_ids], int(params.max_tokens),
+                                   int(eos), salt)
         if lora is None and self.ecfg.prefix_cache:
             self._prompts[rid] = np.asarray(prompt_ids, dtype=np.int32)
         self.params[rid] = params
@@ -253,7 +263,43 @@ class LLMEngine:
         self.traces[rid] = RequestTrace(rid, len(prompt_ids))
         return rid
 
+    def _add_hybrid(self, rid, prompt_ids, params, eos, salt):
+        """Admission of a hybrid-model request: a prefix hit only where a
+        recurrent state was saved, and a chunk split where one will be."""
+        ps = self.bm.page_size
+        toks = [int(t) for t in prompt_ids]
+        npg = (len(toks) - 1) // ps
+        hashes = [int(h) for h in self.bm.chain_hashes(toks, npg, salt)] if npg > 0 else []
+        i = self.state_cache.deepest(hashes)
+        cover = (i + 1) * ps if i >= 0 else 0
+        split = npg * ps if npg * ps > cover else -1
+        self.sched.add_request(rid, toks, int(params.max_tokens), int(eos), salt, cover, True, split)
+        self._hyb[rid] = {"restore": (cover, hashes[i]) if cover else None,
+                          "save": (split, hashes[npg - 1]) if split > 0 else None}
+
+    def _hybrid_before(self, plan):
+        for b, sid in enumerate(plan.seq_ids):
+            h = self._hyb.get(int(sid))
+            if h is None or h["restore"] is None:
+                continue
+            cover, key = h["restore"]
+            h["restore"] = None
+            if int(plan.positions[int(plan.seq_start[b])]) == cover:  # the hit happened
+                self.state_cache.restore(key, self.runner.slots.get(int(sid)))
+
+    def _hybrid_after(self, plan):
+        for b, sid in enumerate(plan.seq_ids):
+            h = self._hyb.get(int(sid))
+            if h is None or h["save"] is None:
+                continue
+            at, key = h["save"]
+            r0, n = int(plan.seq_start[b]), int(plan.seq_ntok[b])
+            if n and int(plan.positions[r0]) + n == at:
+                h["save"] = None
+                self.state_cache.save(key, self.runner.slots.get(int(sid)))
+
     def abort(self, rid: int):
+        self._hyb.pop(rid, None)
         self.sched.abort(rid)
         self._free_state(rid)
         self.images.pop(rid, None)
@@ -276,8 +322,12 @@ class LLMEngine:
         ids = [int(s) for s in plan.seq_ids]
         samp = plan.seq_sample
         params = [self.params[i] for i, s in zip(ids, samp) if s]
+        if self.state_cache is not None:
+            self._hybrid_before(plan)
         with self.profiler.stage("forward"):
             sampled = self.runner.run(plan, self.bm, params)
+        if self.state_cache is not None:
+            self._hybrid_after(plan)
         done = set(int(d) for d in self.sched.commit(plan, sampled.tolist()))
         out = []
         now = time.perf_counter()
@@ -321,6 +371,7 @@ class LLMEngine:
         self.images.pop(rid, None)
         self.params.pop(rid, None)
         self.prompt_len.pop(rid, None)
+        self._hyb.pop(rid, None)
         p = self._prompts.pop(rid, None)
         if p is not None and len(p) >= self.bm.page_size:
             key = p.tobytes()

@@ -10,8 +10,9 @@ caches are kept.  The byte form is a JSON header (geometry, dtype, tokens)
 followed by the raw tensor, so it can go over any transport; `send_prefix` /
 `recv_prefix` move it between torch.distributed ranks.
 
-Hybrid models (linear-attention state) keep no prefix cache, so they export
-nothing.
+Hybrid models (linear-attention state) export nothing: their cached prefixes
+also need the recurrent state saved at the prefix's end, which stays in the
+engine's own state cache (engine/state_cache.py).
 
 `save_prefix_cache` / `load_prefix_cache` persist the whole cache across
 restarts: the snapshots of the engine's recent prompts in one file, stamped
@@ -75,7 +76,7 @@ class PrefixSnapshot:
 def export_prefix(engine, tokens) -> PrefixSnapshot | None:
     """Snapshot of the longest cached run of full pages of `tokens` (None if
     nothing is cached or the engine keeps no prefix cache)."""
-    if not engine.ecfg.prefix_cache:
+    if not engine.ecfg.prefix_cache or getattr(engine, "state_cache", None) is not None:
         return None
     pages = np.asarray(engine.bm.cached_prefix_pages([int(x) for x in tokens]), dtype=np.int64)
     if len(pages) == 0:
@@ -89,8 +90,8 @@ def export_prefix(engine, tokens) -> PrefixSnapshot | None:
 def import_prefix(engine, snap: PrefixSnapshot) -> int:
     """Register the snapshot's pages in this engine's prefix cache; returns
     the number of tokens whose pages were newly imported."""
-    if not engine.ecfg.prefix_cache:
-        raise RuntimeError("this engine keeps no prefix cache")
+    if not engine.ecfg.prefix_cache or getattr(engine, "state_cache", None) is not None:
+        raise RuntimeError("this engine keeps no importable prefix cache")
     d = engine.kv.data
     want = (d.shape[0], 2, snap.n_pages, d.shape[3], d.shape[4], d.shape[5])
     if snap.page_size != engine.bm.page_size or tuple(snap.kv.shape) != want:

@@ -180,3 +180,26 @@ def test_hybrid_model_matches_cpu_oracle():
     st_g, st_c = kvg.ssm_state(0)[1].cpu(), kvc.ssm_state(0)[1]
     rel = float((st_g - st_c).norm() / st_c.norm())
     assert rel < 2e-2, rel
+
+
+def test_hybrid_prefix_hit_gpu():
+    """Hybrid model on the GPU engine: the recurrent state saved at the last
+    page boundary before a prompt's end is restored for a repeat of the
+    prompt, which then gives the same tokens with 48 prompt tokens skipped."""
+    import sys, os
+    sys.path.insert(0, os.path.dirname(__file__))
+    from test_hybrid_cpu import tiny_hybrid
+    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = tiny_hybrid()
+    ec = EngineConfig(max_model_len=128, max_running=4, max_step_tokens=64, prefill_chunk=64,
+                      graph_sizes=(1, 2, 4))
+    eng = LLMEngine.from_config(cfg, DEV, ec, source=RandomSource(cfg, seed=4))
+    p = np.random.default_rng(3).integers(0, cfg.vocab, 53).tolist()
+    sp = SamplingParams(max_tokens=6)
+    o1 = eng.generate([p], sp)[0].token_ids
+    assert eng.state_cache.saves == 1
+    hits0 = eng.bm.prefix_hit_tokens
+    o2 = eng.generate([p], sp)[0].token_ids
+    assert eng.bm.prefix_hit_tokens - hits0 == 48 and eng.state_cache.restores == 1
+    assert o1 == o2
