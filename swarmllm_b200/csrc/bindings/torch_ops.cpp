@@ -265,6 +265,17 @@ void sample(Tensor logits, Tensor temperature, OptT top_k, OptT top_p, OptT seed
                 ptr_or_null<int32_t>(positions), out.data_ptr<int32_t>(), cur_stream());
 }
 
+void apply_penalties(Tensor logits, Tensor off, Tensor tok, Tensor val) {
+  CHECK_DT(logits, at::kFloat); CHECK_DT(off, at::kInt); CHECK_DT(tok, at::kInt);
+  CHECK_DT(val, at::kFloat);
+  TORCH_CHECK(off.numel() == logits.size(0) + 1 && tok.numel() == val.numel(),
+              "penalty table shape");
+  const at::cuda::CUDAGuard guard(logits.device());
+  launch_apply_penalties(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1),
+                         (int)logits.stride(0), off.data_ptr<int32_t>(), tok.data_ptr<int32_t>(),
+                         val.data_ptr<float>(), cur_stream());
+}
+
 void philox_uniform(int64_t seed, Tensor positions, int64_t V, Tensor out) {
   const at::cuda::CUDAGuard guard(out.device());
   launch_philox_uniform((uint64_t)seed, positions.data_ptr<int32_t>(), (int)positions.numel(),
@@ -436,6 +447,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax);
   m.def("sample", &sample);
   m.def("philox_uniform", &philox_uniform);
+  m.def("apply_penalties", &apply_penalties);
   register_moe_ops(m);
   register_ep_ops(m);
 }

@@ -95,6 +95,8 @@ void launch_sample(const float* logits, int rows, int V, int stride, const float
                    const int32_t* positions, int32_t* out, cudaStream_t s);
 void launch_philox_uniform(uint64_t seed, const int32_t* positions, int n_pos, int V, float* out,
                            cudaStream_t s);
+void launch_apply_penalties(float* logits, int rows, int V, int stride, const int32_t* off,
+                            const int32_t* tok, const float* val, cudaStream_t s);
 
 // ---- mixture of experts (moe_tc.cu) -----------------------------------------
 // fmt: 0 = Q4_K experts (fp16 activations), 1 = MXFP4 experts (bf16 activations)

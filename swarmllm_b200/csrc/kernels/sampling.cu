@@ -241,6 +241,21 @@ __global__ void __launch_bounds__(1024) sample_kernel(
   if (threadIdx.x == 0) out[r] = best.i;
 }
 
+// Frequency / presence penalties: row r subtracts val[i] from logit tok[i]
+// for i in [off[r], off[r + 1]) -- the distinct tokens the row's request has
+// generated, val = count * frequency_penalty + presence_penalty.  Tokens of a
+// row are distinct, so the stores never collide.
+__global__ void apply_penalties_kernel(float* __restrict__ logits, int V, int stride,
+                                       const int32_t* __restrict__ off,
+                                       const int32_t* __restrict__ tok,
+                                       const float* __restrict__ val) {
+  const int r = blockIdx.x;
+  for (int i = off[r] + threadIdx.x; i < off[r + 1]; i += blockDim.x) {
+    const int t = tok[i];
+    if ((unsigned)t < (unsigned)V) logits[(size_t)r * stride + t] -= val[i];
+  }
+}
+
 __global__ void philox_uniform_kernel(uint64_t seed, const int32_t* positions, int n_pos, int V,
                                       float* out) {
   const int r = blockIdx.y;
@@ -275,6 +290,13 @@ void launch_sample(const float* logits, int rows, int V, int stride, const float
   if (rows <= 0) return;
   sample_kernel<<<rows, 1024, 0, s>>>(logits, V, stride, temperature, top_k, top_p, seeds,
                                       positions, out);
+  SW_LAUNCH_CHECK();
+}
+
+void launch_apply_penalties(float* logits, int rows, int V, int stride, const int32_t* off,
+                            const int32_t* tok, const float* val, cudaStream_t s) {
+  if (rows <= 0) return;
+  apply_penalties_kernel<<<rows, 128, 0, s>>>(logits, V, stride, off, tok, val);
   SW_LAUNCH_CHECK();
 }
 

@@ -117,6 +117,7 @@ class LLMEngine:
         self.sched = N.Scheduler(self.bm, ecfg.max_step_tokens, ecfg.max_running, ecfg.prefill_chunk)
         self.state_cache = None
         self._hyb: dict[int, dict] = {}     # hybrid requests: pending state restore / save
+        self._gen_counts: dict[int, collections.Counter] = {}  # penalized requests' outputs
         if lin is not None and ecfg.prefix_cache:
             from .state_cache import StateCache
             self.state_cache = StateCache(self.kv, ecfg.state_cache_entries)
@@ -259,6 +260,8 @@ class LLMEngine:
         if lora is None and self.ecfg.prefix_cache:
             self._prompts[rid] = np.asarray(prompt_ids, dtype=np.int32)
         self.params[rid] = params
+        if params.penalized:
+            self._gen_counts[rid] = collections.Counter()
         self.prompt_len[rid] = len(prompt_ids)
         self.traces[rid] = RequestTrace(rid, len(prompt_ids))
         return rid
@@ -300,6 +303,7 @@ class LLMEngine:
 
     def abort(self, rid: int):
         self._hyb.pop(rid, None)
+        self._gen_counts.pop(rid, None)
         self.sched.abort(rid)
         self._free_state(rid)
         self.images.pop(rid, None)
@@ -322,10 +326,12 @@ class LLMEngine:
         ids = [int(s) for s in plan.seq_ids]
         samp = plan.seq_sample
         params = [self.params[i] for i, s in zip(ids, samp) if s]
+        history = ([self._gen_counts.get(i) for i, s in zip(ids, samp) if s]
+                   if self._gen_counts else None)
         if self.state_cache is not None:
             self._hybrid_before(plan)
         with self.profiler.stage("forward"):
-            sampled = self.runner.run(plan, self.bm, params)
+            sampled = self.runner.run(plan, self.bm, params, history)
         if self.state_cache is not None:
             self._hybrid_after(plan)
         done = set(int(d) for d in self.sched.commit(plan, sampled.tolist()))
@@ -337,6 +343,9 @@ class LLMEngine:
                 continue
             tok = int(sampled[k])
             k += 1
+            cnt = self._gen_counts.get(i)
+            if cnt is not None:
+                cnt[tok] += 1
             tr = self.traces.get(i)
             if tr is not None:
                 tr.on_token(now)
@@ -372,6 +381,7 @@ class LLMEngine:
         self.params.pop(rid, None)
         self.prompt_len.pop(rid, None)
         self._hyb.pop(rid, None)
+        self._gen_counts.pop(rid, None)
         p = self._prompts.pop(rid, None)
         if p is not None and len(p) >= self.bm.page_size:
             key = p.tobytes()

@@ -262,14 +262,18 @@ class GpuRunner:
             self.d_ssm[:B, 3] = 0
 
     # ------------------------------------------------------------------ step
-    def run(self, plan, block_manager, params: list[SamplingParams]) -> np.ndarray:
+    def run(self, plan, block_manager, params: list[SamplingParams],
+            history: list | None = None) -> np.ndarray:
+        """`history`: per sampled row, the request's generated-token counts
+        (for frequency / presence penalties) or None."""
         tokens, positions, slots, bt_rows, seq_lens, sample_rows = plan_arrays(
             plan, block_manager, self.max_pages)
         N, S = len(tokens), len(sample_rows)
         if N == 0:
             return np.zeros(0, np.int32)
         decode_only = plan.n_prefill_tokens == 0 and N == S
-        greedy = all(p.greedy for p in params)
+        # the captured graphs end in argmax: penalized rows take the eager path
+        greedy = all(p.greedy and not p.penalized for p in params)
         B = next((b for b in self.graph_sizes if b >= N), None) if decode_only else None
         table = ssm_table(plan, positions, self.slots) if self.slots is not None else None
         if B is not None and B in self.graphs and greedy:
@@ -297,7 +301,7 @@ class GpuRunner:
                 b.embed_rows = torch.from_numpy(ir[0]).to(self.device)
                 b.embed_vals = ir[1].to(self.device)
             logits = self.model.forward(b, self.kv, self.ctx)
-            res = self.sampler.sample(logits, params, positions[sample_rows] if S else [])
+            res = self.sampler.sample(logits, params, positions[sample_rows] if S else [], history)
         self.h_out[:S].copy_(res, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         self.d2h_bytes = 4 * S
@@ -328,9 +332,10 @@ class CpuRunner:
             b.embed_vals = ir[1].cpu()
         return self.model.forward(b, self.kv, None, h_in), positions, sample_rows
 
-    def run(self, plan, block_manager, params: list[SamplingParams]) -> np.ndarray:
+    def run(self, plan, block_manager, params: list[SamplingParams],
+            history: list | None = None) -> np.ndarray:
         if len(plan) == 0:
             return np.zeros(0, np.int32)
         logits, positions, sample_rows = self.forward_plan(plan, block_manager)
         self.last_logits = logits
-        return sample_host(logits, params, positions[sample_rows])
+        return sample_host(logits, params, positions[sample_rows], history)

@@ -24,10 +24,35 @@ class SamplingParams:
     seed: int = 0
     eos_token_id: int = -1
     ignore_eos: bool = False
+    frequency_penalty: float = 0.0   # per occurrence in the completion so far
+    presence_penalty: float = 0.0    # once for any token the completion contains
 
     @property
     def greedy(self) -> bool:
         return self.temperature <= 0.0
+
+    @property
+    def penalized(self) -> bool:
+        return self.frequency_penalty != 0.0 or self.presence_penalty != 0.0
+
+
+def penalty_table(params: list[SamplingParams], history: list | None):
+    """CSR table (row offsets int32 [S + 1], tokens int32, values f32) of the
+    logit penalties of each sampled row: for every distinct token t the
+    request generated so far (the prompt excluded), count(t) *
+    frequency_penalty + presence_penalty, subtracted from the raw logit before
+    temperature.  None when no row is penalized.
+    Reference behaviour: src/inference/sampling.rs:75-125."""
+    if history is None or not any(p.penalized for p in params):
+        return None
+    off, tok, val = [0], [], []
+    for p, h in zip(params, history):
+        if p.penalized and h:
+            for t, c in h.items():
+                tok.append(int(t))
+                val.append(c * p.frequency_penalty + p.presence_penalty)
+        off.append(len(tok))
+    return (np.asarray(off, np.int32), np.asarray(tok, np.int32), np.asarray(val, np.float32))
 
 
 class DeviceSampler:
@@ -49,8 +74,13 @@ class DeviceSampler:
         C().argmax(logits, out, None)
         return out
 
-    def sample(self, logits: torch.Tensor, params: list[SamplingParams], positions: np.ndarray) -> torch.Tensor:
+    def sample(self, logits: torch.Tensor, params: list[SamplingParams], positions: np.ndarray,
+               history: list | None = None) -> torch.Tensor:
         S = logits.shape[0]
+        pen = penalty_table(params, history)
+        if pen is not None:
+            d = [torch.from_numpy(a).to(self.device, non_blocking=True) for a in pen]
+            C().apply_penalties(logits, *d)
         if all(p.greedy for p in params):
             return self.greedy(logits)
         t = torch.tensor([p.temperature for p in params], dtype=torch.float32)
@@ -90,10 +120,18 @@ def philox_uniform_host(seed: int, position: int, tokens: np.ndarray) -> np.ndar
     return (((c0 >> 8).astype(np.float64) + 0.5) / 16777216.0).astype(np.float32)
 
 
-def sample_host(logits: torch.Tensor, params: list[SamplingParams], positions) -> np.ndarray:
+def sample_host(logits: torch.Tensor, params: list[SamplingParams], positions,
+                history: list | None = None) -> np.ndarray:
     """CPU token selection with the same rules as the device kernel."""
     out = np.zeros(logits.shape[0], dtype=np.int32)
-    L = logits.detach().to(torch.float32).cpu().numpy()
+    L = logits.detach().to(torch.float32).cpu().numpy().copy()
+    pen = penalty_table(params, history)
+    if pen is not None:
+        off, tok, val = pen
+        for r in range(len(params)):
+            t, v = tok[off[r]:off[r + 1]], val[off[r]:off[r + 1]]
+            ok = (t >= 0) & (t < L.shape[1])
+            L[r, t[ok]] -= v[ok]
     for r, p in enumerate(params):
         row = L[r]
         if p.greedy:

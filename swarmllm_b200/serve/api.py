@@ -278,7 +278,9 @@ class Serving:
                               top_p=float(body.get("top_p", 1.0) or 1.0),
                               top_k=int(body.get("top_k", 0) or 0),
                               seed=int(body.get("seed", 0) or 0), eos_token_id=int(self.eos),
-                              ignore_eos=bool(body.get("ignore_eos", False)))
+                              ignore_eos=bool(body.get("ignore_eos", False)),
+                              frequency_penalty=float(body.get("frequency_penalty", 0.0) or 0.0),
+                              presence_penalty=float(body.get("presence_penalty", 0.0) or 0.0))
 
     @staticmethod
     def stops(body: dict) -> list[str]:

@@ -428,3 +428,21 @@ def test_stalled_engine_withdraws_readiness():
             assert time.time() - t0 < 6, "readiness did not come back"
             time.sleep(0.05)
     ae.shutdown()
+
+
+def test_penalties_reach_sampling_params():
+    c, ae, eng = _client("hi")
+    seen = []
+    orig = eng.add_request
+
+    def spy(ids, sp, request_id, lora=None):
+        seen.append(sp)
+        return orig(ids, sp, request_id, lora)
+    eng.add_request = spy
+    with c:
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                 "max_tokens": 4, "frequency_penalty": 0.5,
+                                                 "presence_penalty": 1.5})
+        assert r.status_code == 200
+    assert seen[-1].frequency_penalty == 0.5 and seen[-1].presence_penalty == 1.5
+    ae.shutdown()

@@ -397,3 +397,21 @@ def test_philox_matches_host():
     for r in range(3):
         h = philox_uniform_host(987654321, int(pos[r]), np.arange(1000))
         assert np.array_equal(out[r].cpu().numpy(), h)
+
+
+def test_apply_penalties_kernel():
+    import collections
+    from swarmllm_b200.engine.sampling import SamplingParams, penalty_table
+    rows, V = 5, 3000
+    logits = torch.randn(rows, V, device=DEV)
+    ref = logits.clone().cpu()
+    ps = [SamplingParams(frequency_penalty=0.3 * r, presence_penalty=0.5) for r in range(rows)]
+    hist = [collections.Counter({(17 * r + 3 * i) % V: i + 1 for i in range(40 * r)})
+            for r in range(rows)]
+    off, tok, val = penalty_table(ps, hist)
+    for r in range(rows):
+        for t, c in hist[r].items():
+            ref[r, t] -= c * ps[r].frequency_penalty + ps[r].presence_penalty
+    C().apply_penalties(logits, *[torch.from_numpy(a).to(DEV) for a in (off, tok, val)])
+    torch.cuda.synchronize()
+    assert torch.allclose(logits.cpu(), ref, atol=1e-5)
