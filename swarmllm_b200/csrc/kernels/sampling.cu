@@ -141,7 +141,75 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   }
 }
 
-// Per row params: temperature (<=0 -> greedy), top_k (<=0 -> off), top_p (>=1 -> off).
+// ---- temperature / top-k / top-p sampling -------------------------------------
+//
+// Semantics (mirrored by the host sampler): keep the tokens whose logit is >=
+// the k-th largest (ties kept); over those, probabilities softmax((l - max) / T);
+// keep the smallest most-probable set whose mass reaches top_p, plus every token
+// tied with its last member; draw by Gumbel-max with Philox noise per
+// (seed, position, token).
+//
+// Two paths, one CTA per row:
+//  * top-k of at most kSampleCand tokens: radix select of the k-th key (4
+//    passes over the row, warp-aggregated counts), the survivors gathered into
+//    shared memory and bitonic-sorted, and the top-p cut and the draw done on
+//    that short list;
+//  * otherwise: radix select of the top-p cut directly on probability mass
+//    (64-bit fixed point, so the shared-memory sums are order-independent and
+//    reruns bit-identical), then one pass drawing over the survivors.
+constexpr int kSampleCand = 2048;
+constexpr double kMassOne = 1099511627776.0;   // 2^40: fixed-point unit of probability mass
+
+// Largest key T with weight(key >= T) >= want among keys >= floor_key; weight 1
+// per token (MASS = false) or its fixed-point probability.
+template <bool MASS>
+SW_DEVICE uint32_t radix_select(const float* __restrict__ row, int V, uint32_t floor_key,
+                                unsigned long long want, float mx, float inv_t, float inv_z,
+                                unsigned long long* hist, uint32_t* prefix_s,
+                                unsigned long long* want_s) {
+  if (threadIdx.x == 0) { *prefix_s = 0; *want_s = want; }
+  const int lane = threadIdx.x & 31;
+  uint32_t mask = 0;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    const uint32_t prefix = *prefix_s;
+    for (int base = 0; base < V; base += blockDim.x) {   // uniform trip count per warp
+      const int i = base + threadIdx.x;
+      int bin = -1;
+      float l = 0.f;
+      if (i < V) {
+        l = row[i];
+        const uint32_t key = float_key(l);
+        if (key >= floor_key && (key & mask) == prefix) bin = (int)((key >> shift) & 255u);
+      }
+      if (MASS) {
+        if (bin >= 0)
+          atomicAdd(&hist[bin], (unsigned long long)((double)(expf((l - mx) * inv_t) * inv_z) * kMassOne));
+      } else {
+        const unsigned same = __match_any_sync(0xffffffffu, bin);
+        if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(&hist[bin], (unsigned long long)__popc(same));
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned long long need = *want_s;
+      unsigned long long acc = 0;
+      int b = 255;
+      for (; b > 0; --b) {
+        if (acc + hist[b] >= need) break;
+        acc += hist[b];
+      }
+      *want_s = need - acc;
+      *prefix_s = prefix | ((uint32_t)b << shift);
+    }
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  return *prefix_s;
+}
+
 __global__ void __launch_bounds__(1024) sample_kernel(
     const float* __restrict__ logits, int V, int stride, const float* __restrict__ temperature,
     const int32_t* __restrict__ top_k, const float* __restrict__ top_p,
@@ -149,9 +217,13 @@ __global__ void __launch_bounds__(1024) sample_kernel(
     int32_t* __restrict__ out) {
   __shared__ float sv[32];
   __shared__ int si[32];
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t prefix_s, want_s;
   __shared__ float red[32];
+  __shared__ unsigned long long hist[256];
+  __shared__ uint32_t prefix_s;
+  __shared__ unsigned long long want_s;
+  __shared__ unsigned long long cand[kSampleCand];   // (key << 32) | ~index, sorted descending
+  __shared__ float cum[kSampleCand];
+  __shared__ int n_s, cut_s;
   const int r = blockIdx.x;
   const float* row = logits + (size_t)r * stride;
   const float temp = temperature[r];
@@ -163,76 +235,109 @@ __global__ void __launch_bounds__(1024) sample_kernel(
     return;
   }
   const float inv_t = 1.f / temp;
-  // Max logit (for the softmax used by top-p).
+  const uint64_t seed = seeds ? seeds[r] : 0ull;
+  const uint32_t pos = positions ? (uint32_t)positions[r] : 0u;
+  int k = top_k ? top_k[r] : 0;
+  if (k >= V) k = 0;
+  const float tp = top_p ? top_p[r] : 1.f;
+
+  uint32_t floor_key = 0;   // keep keys >= floor_key
+  if (k > 0) {
+    floor_key = radix_select<false>(row, V, 0u, (unsigned long long)k, 0.f, 0.f, 0.f, hist,
+                                    &prefix_s, &want_s);
+    if (k <= kSampleCand) {
+      // ---- short-list path: gather, sort, cut, draw -------------------------
+      if (threadIdx.x == 0) n_s = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const uint32_t key = float_key(row[i]);
+        if (key >= floor_key) {
+          const int slot = atomicAdd(&n_s, 1);
+          if (slot < kSampleCand)
+            cand[slot] = ((unsigned long long)key << 32) | (uint32_t)~(uint32_t)i;
+        }
+      }
+      __syncthreads();
+      const int n = n_s;
+      if (n <= kSampleCand) {   // (more only with ties at the k-th key: mass path below)
+        int np2 = 1;
+        while (np2 < n) np2 <<= 1;
+        for (int j = n + threadIdx.x; j < np2; j += blockDim.x) cand[j] = 0ull;
+        __syncthreads();
+        for (int size = 2; size <= np2; size <<= 1) {           // bitonic sort, descending
+          for (int stride2 = size >> 1; stride2 > 0; stride2 >>= 1) {
+            for (int j = threadIdx.x; j < np2; j += blockDim.x) {
+              const int o = j ^ stride2;
+              if (o > j) {
+                const bool desc = (j & size) == 0;
+                const unsigned long long a = cand[j], b = cand[o];
+                if (desc ? (a < b) : (a > b)) { cand[j] = b; cand[o] = a; }
+              }
+            }
+            __syncthreads();
+          }
+        }
+        const float mx = row[~(uint32_t)cand[0]];
+        // probabilities (unnormalised) and their inclusive prefix sums, in sorted order
+        if (threadIdx.x < 32) {
+          float carry = 0.f;
+          for (int c0 = 0; c0 < n; c0 += 32) {
+            const int j = c0 + threadIdx.x;
+            float e = j < n ? expf((row[~(uint32_t)cand[j]] - mx) * inv_t) : 0.f;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const float t = __shfl_up_sync(0xffffffffu, e, o);
+              if ((int)threadIdx.x >= o) e += t;
+            }
+            if (j < n) cum[j] = carry + e;
+            carry += __shfl_sync(0xffffffffu, e, 31);
+          }
+        }
+        if (threadIdx.x == 0) cut_s = n - 1;
+        __syncthreads();
+        if (tp < 1.f) {
+          const float want = tp * cum[n - 1];
+          for (int j = threadIdx.x; j < n; j += blockDim.x)
+            if (cum[j] >= want && (j == 0 || cum[j - 1] < want)) cut_s = j;
+          __syncthreads();
+          const uint32_t ck = (uint32_t)(cand[cut_s] >> 32);   // extend over ties
+          __syncthreads();
+          for (int j = threadIdx.x; j < n; j += blockDim.x)
+            if ((uint32_t)(cand[j] >> 32) == ck && (j == n - 1 || (uint32_t)(cand[j + 1] >> 32) != ck))
+              cut_s = j;
+          __syncthreads();
+        }
+        const int last = cut_s;
+        for (int j = threadIdx.x; j <= last; j += blockDim.x) {
+          const int i = (int)~(uint32_t)cand[j];
+          const float u = philox_uniform(seed, pos, (uint32_t)i);
+          const float g = -logf(-logf(u));
+          best = argmax_merge(best, ArgMax{(row[i] - mx) * inv_t + g, i});
+        }
+        best = block_argmax(best, sv, si);
+        if (threadIdx.x == 0) out[r] = best.i;
+        return;
+      }
+    }
+  }
+  // ---- whole-row path: top-p cut by radix select on probability mass -------
   float mx = -INFINITY;
   for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, row[i]);
   mx = block_max(mx, red);
-  // --- top-k threshold (k-th largest key) by radix select ------------------
-  uint32_t kth_key = 0;  // keep keys >= kth_key
-  const int k = top_k ? top_k[r] : 0;
-  if (k > 0 && k < V) {
-    if (threadIdx.x == 0) { prefix_s = 0; want_s = (uint32_t)k; }
-    uint32_t mask = 0;
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
-      __syncthreads();
-      const uint32_t prefix = prefix_s;
-      for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        uint32_t key = float_key(row[i]);
-        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        uint32_t want = want_s, acc = 0;
-        int b = 255;
-        for (; b > 0; --b) {
-          if (acc + hist[b] >= want) break;
-          acc += hist[b];
-        }
-        want_s = want - acc;
-        prefix_s = prefix | ((uint32_t)b << shift);
-      }
-      mask |= 255u << shift;
-      __syncthreads();
-    }
-    kth_key = prefix_s;
-  }
-  // --- top-p threshold on probabilities by bisection -----------------------
-  float p_lo = 0.f;  // keep tokens with prob >= p_lo
-  const float tp = top_p ? top_p[r] : 1.f;
+  uint32_t cut_key = floor_key;
   if (tp < 1.f) {
     float z = 0.f;
-    for (int i = threadIdx.x; i < V; i += blockDim.x)
-      if (float_key(row[i]) >= kth_key) z += __expf((row[i] - mx) * inv_t);
-    z = block_sum(z, red);
-    float lo = 0.f, hi = 1.f;  // probability thresholds
-    for (int it = 0; it < 24; ++it) {
-      const float mid = 0.5f * (lo + hi);
-      float m = 0.f;
-      for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        if (float_key(row[i]) < kth_key) continue;
-        float p = __expf((row[i] - mx) * inv_t) / z;
-        if (p >= mid) m += p;
-      }
-      m = block_sum(m, red);
-      if (m >= tp) lo = mid; else hi = mid;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float l = row[i];
+      if (float_key(l) >= floor_key) z += expf((l - mx) * inv_t);
     }
-    p_lo = lo;
-  }
-  const uint64_t seed = seeds ? seeds[r] : 0ull;
-  const uint32_t pos = positions ? (uint32_t)positions[r] : 0u;
-  float z = 1.f;
-  if (p_lo > 0.f) {
-    float zz = 0.f;
-    for (int i = threadIdx.x; i < V; i += blockDim.x)
-      if (float_key(row[i]) >= kth_key) zz += __expf((row[i] - mx) * inv_t);
-    z = block_sum(zz, red);
+    z = block_sum(z, red);
+    cut_key = radix_select<true>(row, V, floor_key, (unsigned long long)((double)tp * kMassOne), mx,
+                                 inv_t, 1.f / z, hist, &prefix_s, &want_s);
   }
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     const float l = row[i];
-    if (float_key(l) < kth_key) continue;
-    if (p_lo > 0.f && __expf((l - mx) * inv_t) / z < p_lo) continue;
+    if (float_key(l) < cut_key) continue;
     const float u = philox_uniform(seed, pos, (uint32_t)i);
     const float g = -logf(-logf(u));
     best = argmax_merge(best, ArgMax{(l - mx) * inv_t + g, i});

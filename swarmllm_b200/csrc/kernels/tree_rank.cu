@@ -67,19 +67,33 @@ __global__ void __launch_bounds__(kRankThreads) tree_rank_partial_kernel(
 #pragma unroll
   for (int j = 0; j < K; ++j) { tv[j] = -INFINITY; ti[j] = 0x7fffffff; }
   float m = -INFINITY, s = 0.f;
-  for (int i = lo + threadIdx.x; i < hi; i += kRankThreads) {
-    const float x = r[i];
-    if (x > m) { s = s * __expf(m - x) + 1.f; m = x; } else { s += __expf(x - m); }
-    if (rank_better(x, i, tv[K - 1], ti[K - 1])) {  // insert, keep descending order
-      float cv = x;
-      int ci = i;
+  // four independent loads per step; the running (max, sum-exp) is rescaled
+  // once per step instead of once per element
+  for (int i0 = lo + threadIdx.x; i0 < hi; i0 += 4 * kRankThreads) {
+    float x[4];
 #pragma unroll
-      for (int j = 0; j < K; ++j) {
-        if (rank_better(cv, ci, tv[j], ti[j])) {
-          const float t1 = tv[j];
-          const int t2 = ti[j];
-          tv[j] = cv; ti[j] = ci;
-          cv = t1; ci = t2;
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * kRankThreads;
+      x[u] = i < hi ? r[i] : -INFINITY;
+    }
+    const float m4 = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    if (m4 > m) { s *= __expf(m - m4); m = m4; }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + u * kRankThreads;
+      if (i >= hi) continue;
+      if (m > -INFINITY) s += __expf(x[u] - m);
+      if (rank_better(x[u], i, tv[K - 1], ti[K - 1])) {  // insert, keep descending order
+        float cv = x[u];
+        int ci = i;
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+          if (rank_better(cv, ci, tv[j], ti[j])) {
+            const float t1 = tv[j];
+            const int t2 = ti[j];
+            tv[j] = cv; ti[j] = ci;
+            cv = t1; ci = t2;
+          }
         }
       }
     }
@@ -182,7 +196,8 @@ __global__ void __launch_bounds__(kRankThreads) tree_rank_merge_kernel(
 using namespace swarm;
 
 int tree_rank_slices(int rows, int V) {
-  int S = rows >= 296 ? 1 : (296 + rows - 1) / rows;
+  // about eight 256-thread CTAs per SM (148 SMs), slices of at least 2048 logits
+  int S = rows >= 1184 ? 1 : (1184 + rows - 1) / rows;
   S = S > 64 ? 64 : S;
   const int per = (V + S - 1) / S;
   if (per < 2048) S = (V + 2047) / 2048 > 0 ? (V + 2047) / 2048 : 1;

@@ -16,7 +16,22 @@ from swarmllm_b200.utils.ext import C
 from swarmllm_b200.gguf import quants as Q
 dev = "cuda:0"
 which = sys.argv[1] if len(sys.argv) > 1 else "qgemm"
+TIME = "--time" in sys.argv    # also print the median CUDA-event time of the case's call
 torch.manual_seed(0)
+
+
+def _time(fn, n=50):
+    """Median device time (us) of fn() over n calls after warm-up (inputs in L2 for the
+    sampling cases: the logits a sampler reads were just written by the LM head)."""
+    for _ in range(5):
+        fn()
+    ts = []
+    for _ in range(n):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(); fn(); b.record(); torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3)
+    ts.sort()
+    print(f"{which}: median {ts[len(ts) // 2]:.1f} us over {n} calls")
 
 def rand_q4k(rows, K):
     # random Q4_K blocks generated on the device (valid scales)
@@ -108,6 +123,8 @@ elif which == "tree_rank":  # drafter top-4 over a 128256 vocabulary, 32 sequenc
     rk = torch.zeros(int(C().tree_rank_ws_floats(rows, V, W)), device=dev)
     for _ in range(5):
         C().tree_rank(logits, W, ids, lp, rk)
+    if TIME:
+        _time(lambda: C().tree_rank(logits, W, ids, lp, rk))
 elif which == "sample":     # temperature / top-k / top-p sampling of 32 rows over 128256 tokens
     rows, V = 32, 128256
     logits = torch.randn(rows, V, device=dev) * 3
@@ -119,6 +136,11 @@ elif which == "sample":     # temperature / top-k / top-p sampling of 32 rows ov
     out = torch.zeros(rows, dtype=torch.int32, device=dev)
     for _ in range(5):
         C().sample(logits, temp, topk, topp, seeds, pos, out)
+    if TIME:
+        _time(lambda: C().sample(logits, temp, topk, topp, seeds, pos, out))
+        topk.zero_()           # top-p alone: the whole-row mass path
+        which = "sample (top_p only)"
+        _time(lambda: C().sample(logits, temp, topk, topp, seeds, pos, out))
 elif which == "moe":       # gpt-oss-style experts (32 of 128, MXFP4), batch 64 tokens top-4
     from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
     from swarmllm_b200.ops.moe import MoeExperts, MoeWorkspace, moe_ffn

@@ -78,3 +78,25 @@ def test_tree_rank_matches_torch(rows, V, k):
         assert torch.equal(got[1:], ref_ix[1:]) and torch.equal(got[0, 2:], ref_ix[0, 2:])
         assert ids.view(rows, k)[0, 0].item() == 17 and ids.view(rows, k)[0, 1].item() == 23
         assert torch.allclose(lp.view(rows, k).cpu().double(), ref_lp, atol=1e-4)
+
+
+def test_ngram_spec_matches_target_greedy_and_accepts_repeats():
+    from swarmllm_b200.engine.ngram_spec import NgramSpecDecoder
+    from swarmllm_b200.models.llama import LlamaGPU
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = _cfg()
+    rng = np.random.default_rng(2)
+    unit = rng.integers(0, cfg.vocab, 12).tolist()
+    prompts = [unit * 4, rng.integers(0, cfg.vocab, 30).tolist()]
+    spec = NgramSpecDecoder(LlamaGPU(cfg, RandomSource(cfg, seed=7), DEV), depth=5,
+                            max_seqs=2, max_model_len=200, prefill_chunk=64)
+    out = spec.generate(prompts, 24)
+    ref = _greedy_reference(cfg, 7, prompts, 24)
+    agree = np.mean([a == b for o, r in zip(out, ref) for a, b in zip(o, r)])
+    assert agree >= 0.95, (agree, out, ref)
+    assert all(len(o) == 24 for o in out)
+    # a draft that would have been right anywhere must have been accepted somewhere
+    from swarmllm_b200.engine.ngram_spec import ngram_draft
+    right = any(ngram_draft(p + r[:i], 3, 1) == [r[i]]
+                for p, r in zip(prompts, ref) for i in range(1, 24))
+    assert spec.stats.accepted > 0 or not right, (spec.stats, out)
