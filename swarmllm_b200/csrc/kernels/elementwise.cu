@@ -66,7 +66,31 @@ __global__ void epi_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ resid
   const int dim = g.rows;
   float* rr = residual + (size_t)t * dim;
   float ss = 0.f;
-  if ((dim & 3) == 0 && (reinterpret_cast<uintptr_t>(residual) & 15) == 0) {
+  const bool vec8 = (dim & 7) == 0 && (reinterpret_cast<uintptr_t>(residual) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
+  if (vec8) {
+    // eight rows per thread and step: one partial-sum lookup per eight, 16-byte accesses
+    for (int i = 8 * threadIdx.x; i < dim; i += 8 * kThreads) {
+      float4 g0, g1;
+      g.get8(t, i, g0, g1);
+      float4 v0 = *reinterpret_cast<const float4*>(rr + i);
+      float4 v1 = *reinterpret_cast<const float4*>(rr + i + 4);
+      if (bias) {
+        const float4 b0 = *reinterpret_cast<const float4*>(bias + i);
+        const float4 b1 = *reinterpret_cast<const float4*>(bias + i + 4);
+        g0.x += b0.x; g0.y += b0.y; g0.z += b0.z; g0.w += b0.w;
+        g1.x += b1.x; g1.y += b1.y; g1.z += b1.z; g1.w += b1.w;
+      }
+      v0.x += g0.x; v0.y += g0.y; v0.z += g0.z; v0.w += g0.w;
+      v1.x += g1.x; v1.y += g1.y; v1.z += g1.z; v1.w += g1.w;
+      *reinterpret_cast<float4*>(rr + i) = v0;
+      *reinterpret_cast<float4*>(rr + i + 4) = v1;
+      *reinterpret_cast<float4*>(row + i) = v0;
+      *reinterpret_cast<float4*>(row + i + 4) = v1;
+      ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w +
+            v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
+    }
+  } else if ((dim & 3) == 0 && (reinterpret_cast<uintptr_t>(residual) & 15) == 0) {
     // four rows per thread and step: 16-byte loads, more bytes in flight
     for (int i = 4 * threadIdx.x; i < dim; i += 4 * kThreads) {
       const float4 gv = g.get4(t, i);
@@ -90,8 +114,25 @@ __global__ void epi_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ resid
   if (out == nullptr) return;
   ss = block_sum(ss, red);
   const float inv = rsqrtf(ss / dim + eps);
+  __half* o = out + (size_t)t * out_stride;
+  if (vec8 && (out_stride & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+    for (int i = 8 * threadIdx.x; i < dim; i += 8 * kThreads) {
+      const float4 a0 = *reinterpret_cast<const float4*>(row + i);
+      const float4 a1 = *reinterpret_cast<const float4*>(row + i + 4);
+      const float4 w0 = *reinterpret_cast<const float4*>(w + i);
+      const float4 w1 = *reinterpret_cast<const float4*>(w + i + 4);
+      __align__(16) __half y[8] = {
+          __float2half_rn(a0.x * inv * w0.x), __float2half_rn(a0.y * inv * w0.y),
+          __float2half_rn(a0.z * inv * w0.z), __float2half_rn(a0.w * inv * w0.w),
+          __float2half_rn(a1.x * inv * w1.x), __float2half_rn(a1.y * inv * w1.y),
+          __float2half_rn(a1.z * inv * w1.z), __float2half_rn(a1.w * inv * w1.w)};
+      *reinterpret_cast<uint4*>(o + i) = *reinterpret_cast<const uint4*>(y);
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < dim; i += kThreads)
-    out[(size_t)t * out_stride + i] = __float2half_rn(row[i] * inv * w[i]);
+    o[i] = __float2half_rn(row[i] * inv * w[i]);
 }
 
 // Grid (token, group of kRopeHpb heads) over the head list [q | k | v].
@@ -221,6 +262,31 @@ __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int
                                   int interleaved, float alpha, float limit,
                                   __half* __restrict__ out) {
   const int t = blockIdx.y;
+  if (!interleaved && (F & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
+    // eight features per thread and step: one partial-sum lookup per eight, 16-byte stores
+    for (int i = 8 * (blockIdx.x * blockDim.x + threadIdx.x); i < F; i += 8 * gridDim.x * blockDim.x) {
+      float4 g0, g1, u0, u1;
+      g.get8(t, i, g0, g1);
+      g.get8(t, F + i, u0, u1);
+      const float gs[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float us[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      __align__(16) __half y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float gv = gs[e] + (bias ? bias[i + e] : 0.f);
+        float uv = us[e] + (bias ? bias[F + i + e] : 0.f);
+        if (kind == 0) {
+          y[e] = __float2half_rn(__fdividef(gv, 1.f + __expf(-gv)) * uv);
+        } else {
+          gv = fminf(gv, limit);
+          uv = fminf(fmaxf(uv, -limit), limit);
+          y[e] = __float2half_rn(__fdividef(gv, 1.f + __expf(-alpha * gv)) * (uv + 1.f));
+        }
+      }
+      *reinterpret_cast<uint4*>(out + (size_t)t * F + i) = *reinterpret_cast<const uint4*>(y);
+    }
+    return;
+  }
   if (!interleaved && (F & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0) {
     // four features per thread and step, 16-byte loads
     for (int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x); i < F; i += 4 * gridDim.x * blockDim.x) {
@@ -400,7 +466,10 @@ void launch_epi_rope_kv(const GemmOut& g, const float* bias, const int32_t* posi
 void launch_epi_swiglu(const GemmOut& g, const float* bias, int F, int kind, int interleaved,
                        float alpha, float limit, __half* out, cudaStream_t s) {
   if (g.T <= 0) return;
-  dim3 grid((F + 255) / 256 < 64 ? (F + 255) / 256 : 64, g.T);
+  // one step per thread on the vector paths (8 or 4 features), else one feature
+  const int per = (!interleaved && (F & 7) == 0) ? 8 : (!interleaved && (F & 3) == 0) ? 4 : 1;
+  const int need = (F + per * 256 - 1) / (per * 256);
+  dim3 grid(need < 64 ? need : 64, g.T);
   epi_swiglu_kernel<<<grid, 256, 0, s>>>(g, bias, F, kind, interleaved, alpha, limit, out);
   SW_LAUNCH_CHECK();
 }

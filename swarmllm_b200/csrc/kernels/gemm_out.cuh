@@ -100,6 +100,44 @@ struct GemmOut {
     }
     return acc;
   }
+
+  // Rows r .. r + 7 of token t (r a multiple of 8: one 128-row tile, so one
+  // segment lookup serves all eight).
+  __device__ __forceinline__ void get8(int t, int r, float4& lo, float4& hi) const {
+    lo = make_float4(0.f, 0.f, 0.f, 0.f);
+    hi = lo;
+    if (add) {
+      const float* a = add + (size_t)t * add_stride + r;
+      lo = make_float4(a[0], a[1], a[2], a[3]);
+      hi = make_float4(a[4], a[5], a[6], a[7]);
+    }
+    const float* base;
+    if (mode == 0) {
+      base = ws + (size_t)t * rows + r;
+      const float4 v0 = *reinterpret_cast<const float4*>(base);
+      const float4 v1 = *reinterpret_cast<const float4*>(base + 4);
+      lo = make_float4(lo.x + v0.x, lo.y + v0.y, lo.z + v0.z, lo.w + v0.w);
+      hi = make_float4(hi.x + v1.x, hi.y + v1.y, hi.z + v1.z, hi.w + v1.w);
+      return;
+    }
+    const int rt = r >> 7, rr = r & 127;
+    const int nt = t >> tok_shift, tt = t & (tok_tile - 1);
+    const int tile = rt * n_tok_tiles + nt;
+    const int u0 = tile * ksb;
+    const int c0 = cta_of(u0);
+    const int c1 = cta_of(u0 + ksb - 1);
+    const int ns = n_src > 1 ? n_src : 1;
+    for (int s = 0; s < ns; ++s) {
+      const float* w = ws + (size_t)s * src_stride;
+      for (int c = c0; c <= c1; ++c) {
+        const float* p = w + ((size_t)(tile + c) * tok_tile + tt) * 128 + rr;
+        const float4 v0 = *reinterpret_cast<const float4*>(p);
+        const float4 v1 = *reinterpret_cast<const float4*>(p + 4);
+        lo.x += v0.x; lo.y += v0.y; lo.z += v0.z; lo.w += v0.w;
+        hi.x += v1.x; hi.y += v1.y; hi.z += v1.z; hi.w += v1.w;
+      }
+    }
+  }
 #endif
 };
 

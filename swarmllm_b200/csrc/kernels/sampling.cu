@@ -175,21 +175,37 @@ SW_DEVICE uint32_t radix_select(const float* __restrict__ row, int V, uint32_t f
     for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
     __syncthreads();
     const uint32_t prefix = *prefix_s;
-    for (int base = 0; base < V; base += blockDim.x) {   // uniform trip count per warp
-      const int i = base + threadIdx.x;
-      int bin = -1;
-      float l = 0.f;
-      if (i < V) {
-        l = row[i];
-        const uint32_t key = float_key(l);
-        if (key >= floor_key && (key & mask) == prefix) bin = (int)((key >> shift) & 255u);
+    // four loads in flight per thread; uniform trip count per warp (the warp
+    // intrinsics below need every lane)
+    for (int base = 0; base < V; base += 4 * blockDim.x) {
+      float l[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = base + u * blockDim.x + threadIdx.x;
+        l[u] = i < V ? row[i] : 0.f;
       }
-      if (MASS) {
-        if (bin >= 0)
-          atomicAdd(&hist[bin], (unsigned long long)((double)(expf((l - mx) * inv_t) * inv_z) * kMassOne));
-      } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = base + u * blockDim.x + threadIdx.x;
+        int bin = -1;
+        if (i < V) {
+          const uint32_t key = float_key(l[u]);
+          if (key >= floor_key && (key & mask) == prefix) bin = (int)((key >> shift) & 255u);
+        }
+        if (!__any_sync(0xffffffffu, bin >= 0)) continue;   // warp-uniform: later passes skip most
         const unsigned same = __match_any_sync(0xffffffffu, bin);
-        if (bin >= 0 && lane == __ffs(same) - 1) atomicAdd(&hist[bin], (unsigned long long)__popc(same));
+        const bool leader = lane == __ffs(same) - 1;
+        if (MASS) {
+          // exact group sum of the 40-bit weights as two 20-bit halves (each < 2^25)
+          const unsigned long long w =
+              bin >= 0 ? (unsigned long long)((double)(expf((l[u] - mx) * inv_t) * inv_z) * kMassOne)
+                       : 0ull;
+          const unsigned lo = __reduce_add_sync(same, (unsigned)(w & 0xFFFFFull));
+          const unsigned hi = __reduce_add_sync(same, (unsigned)(w >> 20));
+          if (bin >= 0 && leader) atomicAdd(&hist[bin], ((unsigned long long)hi << 20) + lo);
+        } else {
+          if (bin >= 0 && leader) atomicAdd(&hist[bin], (unsigned long long)__popc(same));
+        }
       }
     }
     __syncthreads();
@@ -210,7 +226,7 @@ SW_DEVICE uint32_t radix_select(const float* __restrict__ row, int V, uint32_t f
   return *prefix_s;
 }
 
-__global__ void __launch_bounds__(1024) sample_kernel(
+__global__ void __launch_bounds__(1024, 1) sample_kernel(
     const float* __restrict__ logits, int V, int stride, const float* __restrict__ temperature,
     const int32_t* __restrict__ top_k, const float* __restrict__ top_p,
     const uint64_t* __restrict__ seeds, const int32_t* __restrict__ positions,

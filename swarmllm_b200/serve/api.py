@@ -265,6 +265,11 @@ class Serving:
         return len(ids) + (len(images) * (v.rows_per_image - 1) if images and v else 0)
 
     def params(self, body: dict, n_prompt: int) -> SamplingParams:
+        if body.get("logprobs") or body.get("top_logprobs"):
+            # refused rather than ignored, so a client never reads a missing field as "none"
+            # (reference behaviour: src/api/openai/mod.rs:298-311)
+            raise ApiError(400, "logprobs are not returned by this server; remove `logprobs` "
+                                "and `top_logprobs` from the request")
         mt = body.get("max_tokens", body.get("max_completion_tokens", body.get("max_output_tokens")))
         if mt is None:
             mt = max(1, min(1024, self.max_model_len - n_prompt))

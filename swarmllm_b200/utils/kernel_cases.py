@@ -106,6 +106,9 @@ elif which == "rmsnorm":   # down projection + residual-add/RMSNorm epilogue, 20
     out = torch.empty(T, rows, device=dev).half()
     for _ in range(5):
         C().epi_residual_rmsnorm(lin(x, ws), h, None, w, out, 1e-5)
+    if TIME:   # the epilogue alone, over the last GEMM's partial sums
+        g = lin(x, ws)
+        _time(lambda: C().epi_residual_rmsnorm(g, h, None, w, out, 1e-5))
 elif which == "swiglu":    # gate|up projection + SwiGLU epilogue, 2048-token chunk
     from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
     rows, K, T = 57344, 8192, 2048
@@ -115,6 +118,9 @@ elif which == "swiglu":    # gate|up projection + SwiGLU epilogue, 2048-token ch
     act = torch.empty(T, rows // 2, device=dev).half()
     for _ in range(5):
         C().epi_swiglu(lin(x, ws), None, rows // 2, 0, False, 0.0, 0.0, act)
+    if TIME:   # the epilogue alone, over the last GEMM's partial sums
+        g = lin(x, ws)
+        _time(lambda: C().epi_swiglu(g, None, rows // 2, 0, False, 0.0, 0.0, act))
 elif which == "tree_rank":  # drafter top-4 over a 128256 vocabulary, 32 sequences x width 4
     rows, V, W = 128, 128256, 4
     logits = torch.randn(rows, V, device=dev) * 3

@@ -446,3 +446,17 @@ def test_penalties_reach_sampling_params():
         assert r.status_code == 200
     assert seen[-1].frequency_penalty == 0.5 and seen[-1].presence_penalty == 1.5
     ae.shutdown()
+
+
+def test_logprobs_refused_not_ignored():
+    c, ae, eng = _client("hi")
+    with c:
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                 "logprobs": True, "top_logprobs": 3})
+        assert r.status_code == 400 and "logprobs" in r.text
+        r = c.post("/v1/completions", json={"prompt": "x", "logprobs": 2, "max_tokens": 2})
+        assert r.status_code == 400
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}],
+                                                 "logprobs": False, "max_tokens": 2})
+        assert r.status_code == 200
+    ae.shutdown()

@@ -445,3 +445,59 @@ def test_sampling_paths_match_host(ties):
     agree = (out.cpu().numpy() == host).mean()
     # float32 (device) and float64 (host) cumulative mass may straddle a cut
     assert agree >= (11 / 12 if ties else 1.0), (out.cpu().tolist(), host.tolist())
+
+
+@pytest.mark.parametrize("T", [1, 40])
+@pytest.mark.parametrize("kind", [0, 1])
+def test_swiglu_on_stream_k_partials(T, kind):
+    """SwiGLU epilogue (8-wide path) reading a Q4_K GEMM's stream-K partial
+    sums, against the fp32 reference of GEMM + activation."""
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    F, K = 1280, 2048
+    rng = np.random.default_rng(F + T + kind)
+    w = rng.standard_normal((2 * F, K), dtype=np.float32) * 0.02
+    b = Q.quantize(w, Q.Q4_K)
+    wd = torch.from_numpy(Q.dequantize(b, Q.Q4_K))
+    x = _x(T, K, seed=T)
+    v = x.float() @ wd.T
+    gg, uu = v[:, :F], v[:, F:]
+    if kind == 0:
+        ref = torch.nn.functional.silu(gg) * uu
+    else:
+        xg, u = gg.clamp(max=7.0), uu.clamp(-7.0, 7.0)
+        ref = xg * torch.sigmoid(1.702 * xg) * (u + 1)
+    lin = QLinear(b, Q.Q4_K, 2 * F, K, DEV)
+    ws = GemmWorkspace(DEV, T, 2 * F)
+    out = torch.empty(T, F, dtype=torch.float16, device=DEV)
+    C().epi_swiglu(lin(x.to(DEV), ws), None, F, kind, False, 1.702, 7.0, out)
+    torch.cuda.synchronize()
+    ws.check()
+    assert rel_err(out.float().cpu(), ref) < 4e-3
+
+
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_residual_rmsnorm_rows_path(with_bias):
+    """Residual add + RMSNorm over >= 64 token rows (one CTA per row, 8-wide
+    path) reading a Q4_K GEMM's stream-K partials, against fp32."""
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    T, H, K = 80, 1280, 2048
+    rng = np.random.default_rng(7)
+    w = rng.standard_normal((H, K), dtype=np.float32) * 0.02
+    b = Q.quantize(w, Q.Q4_K)
+    wd = torch.from_numpy(Q.dequantize(b, Q.Q4_K))
+    x = _x(T, K, seed=3)
+    res = torch.randn(T, H)
+    bias = torch.randn(H) * 0.1 if with_bias else None
+    nw = torch.rand(H) + 0.5
+    h = res + x.float() @ wd.T + (bias if with_bias else 0)
+    ref = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5) * nw
+    lin = QLinear(b, Q.Q4_K, H, K, DEV)
+    ws = GemmWorkspace(DEV, T, H)
+    rd = res.clone().to(DEV)
+    out = torch.empty(T, H, dtype=torch.float16, device=DEV)
+    C().epi_residual_rmsnorm(lin(x.to(DEV), ws), rd, bias.to(DEV) if with_bias else None,
+                             nw.to(DEV), out, 1e-5)
+    torch.cuda.synchronize()
+    ws.check()
+    assert rel_err(rd.cpu(), h) < 3e-3
+    assert rel_err(out.float().cpu(), ref) < 4e-3
