@@ -3,7 +3,11 @@
   serve     OpenAI/Anthropic/Responses/MCP HTTP server on :8800 (reference: `swarmllm run`)
   generate  one-shot generation from token ids or text
   bench     single-GPU tokens/s over a preset (reference: `swarmllm bench`)
+  chat      interactive chat with a local model (reference: `swarmllm chat`)
   info      model / GGUF summary
+  status    a running node's status and readiness (reference: `swarmllm status`)
+  diagnostics  GPUs, NVML readings (read-only), native extensions, versions
+  test-split   the tiny Llama split over 2 CPU processes vs one (reference: `swarmllm test-split`)
   shard     split a GGUF into the sharded checkpoint layout
   make-gguf write a random-init GGUF of a preset (test models)
 
@@ -54,10 +58,50 @@ def _tokenizer(args, eng):
     return ByteTokenizer(eng.cfg.vocab), None
 
 
+def node_status(url: str, api_key: str | None = None) -> dict:
+    """GET a running node's /api/status and /health/ready."""
+    import urllib.error
+    import urllib.request
+    hdr = {"Authorization": f"Bearer {api_key}"} if api_key else {}
+    out = {"url": url}
+    for key, path in (("status", "/api/status"), ("ready", "/health/ready")):
+        try:
+            with urllib.request.urlopen(urllib.request.Request(url.rstrip("/") + path, headers=hdr),
+                                        timeout=5) as r:
+                out[key] = json.loads(r.read().decode() or "null")
+        except urllib.error.HTTPError as e:
+            out[key] = {"http_status": e.code}
+        except OSError as e:
+            out[key] = {"error": str(e)}
+    return out
+
+
+def chat_loop(eng, tok, template, args, fin, fout):
+    """Read user turns from `fin`, answer each with the full conversation so
+    far; an empty line or EOF ends the session."""
+    from .engine.sampling import SamplingParams
+    from .serve.chat_template import render
+    msgs = [{"role": "system", "content": args.system}] if args.system else []
+    while True:
+        fout.write("> ")
+        fout.flush()
+        line = fin.readline()
+        if not line or not line.strip():
+            return
+        msgs.append({"role": "user", "content": line.rstrip("\n")})
+        ids = tok.encode(render(msgs, eng.cfg.arch, template))
+        sp = SamplingParams(max_tokens=args.max_tokens, temperature=args.temperature,
+                            eos_token_id=getattr(tok, "eos_id", -1))
+        out = eng.generate([ids], sp)[0].token_ids
+        text = tok.decode([t for t in out if t != sp.eos_token_id])
+        fout.write(text + "\n")
+        msgs.append({"role": "assistant", "content": text})
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(prog="swarmllm_b200")
     sub = p.add_subparsers(dest="cmd", required=True)
-    for name in ("serve", "generate", "bench", "info"):
+    for name in ("serve", "generate", "bench", "info", "chat"):
         s = sub.add_parser(name)
         s.add_argument("--model", default="llama-3.2-3b")
         s.add_argument("--gguf", default=None)
@@ -90,10 +134,20 @@ def main(argv=None):
             s.add_argument("--max-tokens", type=int, default=32)
             s.add_argument("--temperature", type=float, default=0.0)
             s.add_argument("--adapter", default=None, help="name of a --lora adapter to generate with")
+        if name == "chat":
+            s.add_argument("--max-tokens", type=int, default=256)
+            s.add_argument("--temperature", type=float, default=0.7)
+            s.add_argument("--system", default=None)
         if name == "bench":
             s.add_argument("--batch", type=int, default=8)
             s.add_argument("--prompt-len", type=int, default=512)
             s.add_argument("--gen", type=int, default=64)
+    s = sub.add_parser("status")
+    s.add_argument("--url", default="http://127.0.0.1:8800")
+    s.add_argument("--api-key", default=os.environ.get("SWARMLLM_API_KEY"))
+    sub.add_parser("diagnostics")
+    s = sub.add_parser("test-split")
+    s.add_argument("--world", type=int, default=2)
     s = sub.add_parser("shard")
     s.add_argument("gguf")
     s.add_argument("out_dir")
@@ -104,6 +158,19 @@ def main(argv=None):
     s.add_argument("--seed", type=int, default=0)
     args = p.parse_args(argv)
 
+    if args.cmd == "status":
+        print(json.dumps(node_status(args.url, args.api_key), indent=1))
+        return
+    if args.cmd == "diagnostics":
+        from .utils.diagnostics import collect
+        print(json.dumps(collect(), indent=1))
+        return
+    if args.cmd == "test-split":
+        from .parallel.split_check import split_check
+        r = split_check(world=args.world)
+        r.pop("tokens")
+        print(json.dumps(r))
+        sys.exit(0 if r["ok"] else 1)
     if args.cmd == "shard":
         from .gguf.file import write_sharded
         m = write_sharded(args.gguf, args.out_dir, args.layers_per_shard)
@@ -140,6 +207,10 @@ def main(argv=None):
                          eng.save_prefix_cache(args.kv_persist), args.kv_persist)
         return
     from .engine.sampling import SamplingParams
+    if args.cmd == "chat":
+        tok, tpl = _tokenizer(args, eng)
+        chat_loop(eng, tok, tpl, args, sys.stdin, sys.stdout)
+        return
     if args.cmd == "generate":
         tok, _ = _tokenizer(args, eng)
         ids = [int(x) for x in args.ids.split(",")] if args.ids else tok.encode(args.prompt)
