@@ -47,13 +47,15 @@ def _worker(rank, world, port):
         tp = TpGroup(rank, world, dev)
         m_tp = LlamaGPU(cfg, RandomSource(cfg, seed=3), dev, tp=tp)
         m_1 = LlamaGPU(cfg, RandomSource(cfg, seed=3), dev)
-        c_tp, c_1 = m_tp.make_context(64, 64, 256), m_1.make_context(64, 64, 256)
+        c_tp, c_1 = m_tp.make_context(128, 128, 256), m_1.make_context(128, 128, 256)
         kv_tp = PagedKVCache(cfg.n_layers, 8, m_tp.n_kv, cfg.head_dim, dev)
         kv_1 = PagedKVCache(cfg.n_layers, 8, cfg.n_kv_heads, cfg.head_dim, dev)
         rng = np.random.default_rng(0)
-        toks = rng.integers(0, cfg.vocab, 43)
-        bt = np.tile(np.arange(8, dtype=np.int32), (64, 1))
-        for lo, hi in ((0, 40), (40, 41), (41, 42), (42, 43)):
+        toks = rng.integers(0, cfg.vocab, 83)
+        bt = np.tile(np.arange(8, dtype=np.int32), (128, 1))
+        # 80 rows: the one-CTA-per-row residual/RMSNorm epilogue summing both ranks' partials;
+        # then decode rows: the cluster variant
+        for lo, hi in ((0, 80), (80, 81), (81, 82), (82, 83)):
             pos = np.arange(lo, hi)
             rows = list(range(hi - lo))
             a = m_tp.forward(_batch(toks[lo:hi], pos, bt[:hi - lo], dev, rows), kv_tp, c_tp)
