@@ -14,6 +14,7 @@ plus ModelProcessPool::generate (src/inference/process_pool.rs:14208).
 from __future__ import annotations
 
 import collections
+import dataclasses
 import hashlib
 import itertools
 import time
@@ -334,6 +335,8 @@ class LLMEngine:
             sampled = self.runner.run(plan, self.bm, params, history)
         if self.state_cache is not None:
             self._hybrid_after(plan)
+        if any(p.constraint is not None for p in params):
+            sampled = self._constrain(params, sampled)
         done = set(int(d) for d in self.sched.commit(plan, sampled.tolist()))
         out = []
         now = time.perf_counter()
@@ -352,6 +355,29 @@ class LLMEngine:
             out.append((i, tok, i in done))
         self.steps += 1
         return out
+
+    CONSTRAINT_CANDIDATES = 64
+
+    def _constrain(self, params, sampled):
+        """Apply per-request token constraints to the sampled rows: keep the
+        drawn token if allowed, else the best allowed candidate by logit (the
+        top 64, then the whole row).  Runs before the scheduler commits."""
+        sampled = np.array(sampled, copy=True)
+        logits = self.runner.last_logits
+        for k, p in enumerate(params):
+            c = p.constraint
+            if c is None:
+                continue
+            row = logits[k].float()
+            top = torch.topk(row, min(self.CONSTRAINT_CANDIDATES, row.numel())).indices.tolist()
+            t = c.choose(int(sampled[k]), top)
+            if t is None:
+                t = c.choose(int(sampled[k]), torch.argsort(row, descending=True).tolist())
+            if t is None:   # nothing keeps the text valid: end the reply
+                t = p.eos_token_id if p.eos_token_id >= 0 else int(sampled[k])
+            c.accept(t)
+            sampled[k] = t
+        return sampled
 
     def embed_text(self, ids: list[int]) -> list[float]:
         """Mean-pooled, L2-normalised input embeddings of a token list (the
@@ -394,6 +420,9 @@ class LLMEngine:
                  ) -> list[RequestOutput]:
         if not isinstance(params, list):
             params = [params or SamplingParams()] * len(prompts)
+        # a constraint carries per-request state: each request gets its own
+        params = [dataclasses.replace(sp, constraint=sp.constraint.fresh())
+                  if sp.constraint is not None else sp for sp in params]
         rids = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
         pending = set(rids)
         results: dict[int, list[int]] = {r: [] for r in rids}

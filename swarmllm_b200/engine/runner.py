@@ -284,6 +284,7 @@ class GpuRunner:
             g, logits, out = self.graphs[B]
             g.replay()
             res = out[:S]
+            self.last_logits = logits[:S]
         else:
             M, _ = self._upload(tokens, positions, slots, bt_rows, seq_lens, sample_rows)
             ns = self._upload_ssm(table) if table is not None else 0
@@ -301,6 +302,7 @@ class GpuRunner:
                 b.embed_rows = torch.from_numpy(ir[0]).to(self.device)
                 b.embed_vals = ir[1].to(self.device)
             logits = self.model.forward(b, self.kv, self.ctx)
+            self.last_logits = logits
             res = self.sampler.sample(logits, params, positions[sample_rows] if S else [], history)
         self.h_out[:S].copy_(res, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()

@@ -7,7 +7,7 @@ tokens up to logit rounding.  Reference: src/inference/sampling.rs:314,339.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import numpy as np
 import torch
@@ -26,6 +26,9 @@ class SamplingParams:
     ignore_eos: bool = False
     frequency_penalty: float = 0.0   # per occurrence in the completion so far
     presence_penalty: float = 0.0    # once for any token the completion contains
+    # per-request token filter applied before a token is committed (serve/json_guard.py):
+    # .choose(drawn, candidates) -> token or None, .accept(token)
+    constraint: object = field(default=None, compare=False, repr=False)
 
     @property
     def greedy(self) -> bool:

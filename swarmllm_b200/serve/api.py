@@ -241,6 +241,7 @@ class Serving:
         self.ae, self.tok, self.model_name = aengine, tokenizer, model_name
         self.arch, self.template, self.max_model_len = arch, chat_template, max_model_len
         self.eos = getattr(tokenizer, "eos_id", -1)
+        self._pieces: dict[int, str] = {}
         self.started = time.time()
 
     # ---------------------------------------------------------------- request parsing
@@ -279,13 +280,26 @@ class Serving:
             raise ApiError(400, f"prompt ({n_prompt}) + max_tokens ({mt}) exceeds the "
                                 f"context window ({self.max_model_len})")
         t = body.get("temperature")
+        rf = body.get("response_format") or {}
+        constraint = None
+        if isinstance(rf, dict) and rf.get("type") in ("json_object", "json_schema"):
+            from .json_guard import JsonConstraint
+            constraint = JsonConstraint(self.piece, int(self.eos))
         return SamplingParams(max_tokens=int(mt), temperature=float(1.0 if t is None else t),
+                              constraint=constraint,
                               top_p=float(body.get("top_p", 1.0) or 1.0),
                               top_k=int(body.get("top_k", 0) or 0),
                               seed=int(body.get("seed", 0) or 0), eos_token_id=int(self.eos),
                               ignore_eos=bool(body.get("ignore_eos", False)),
                               frequency_penalty=float(body.get("frequency_penalty", 0.0) or 0.0),
                               presence_penalty=float(body.get("presence_penalty", 0.0) or 0.0))
+
+    def piece(self, tok: int) -> str:
+        """Text of one token (cached: the JSON constraint asks for many)."""
+        p = self._pieces.get(tok)
+        if p is None:
+            p = self._pieces[tok] = self.tok.decode([tok])
+        return p
 
     @staticmethod
     def stops(body: dict) -> list[str]:
