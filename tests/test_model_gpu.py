@@ -203,3 +203,27 @@ def test_hybrid_prefix_hit_gpu():
     o2 = eng.generate([p], sp)[0].token_ids
     assert eng.bm.prefix_hit_tokens - hits0 == 48 and eng.state_cache.restores == 1
     assert o1 == o2
+
+
+def test_json_constraint_gpu_graph_path():
+    """JSON-constrained decoding on the GPU engine, decode steps replayed from
+    CUDA graphs (the constraint reads the graph's logits): the text is a valid
+    JSON prefix, and the same for a sampled request."""
+    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from swarmllm_b200.models.weights import RandomSource
+    from swarmllm_b200.serve.json_guard import JsonConstraint, JsonPrefix
+    from swarmllm_b200.serve.tokenizer import ByteTokenizer
+    cfg = _cfg()
+    tok = ByteTokenizer(cfg.vocab)
+    eng = LLMEngine.from_config(cfg, DEV, EngineConfig(max_model_len=256, max_running=4,
+                                                       max_step_tokens=128, prefill_chunk=64,
+                                                       graph_sizes=(1, 2, 4)),
+                                source=RandomSource(cfg, seed=5))
+    prompt = tok.encode("json please")
+    for temp in (0.0, 0.8):
+        sp = SamplingParams(max_tokens=30, temperature=temp, seed=3, eos_token_id=tok.eos_id,
+                            constraint=JsonConstraint(tok.token_str, tok.eos_id))
+        outs = eng.generate([prompt, prompt], sp)
+        for o in outs:
+            text = tok.decode([t for t in o.token_ids if t != tok.eos_id])
+            assert text.lstrip().startswith("{") and JsonPrefix().feed(text), text
