@@ -1,7 +1,8 @@
 """Standalone cases of the hot kernels, for profiling one kernel at a time:
 
     python -m swarmllm_b200.utils.kernel_cases \
-        {qgemm|qgemv|qgemv_o|dense|attn|attn_prefill|rmsnorm|swiglu|moe|delta|tree_rank|sample}
+        {qgemm|qgemv|qgemv_o|dense|attn|attn_prefill|rmsnorm|swiglu|rope_kv|moe|delta|delta_decode|
+         tree_rank|sample} [--time]
 
 Each case builds benchmark-sized operands on cuda:0 (inputs larger than the
 126 MB L2 where memory traffic matters; tree_rank and sample use the real
@@ -121,6 +122,43 @@ elif which == "swiglu":    # gate|up projection + SwiGLU epilogue, 2048-token ch
     if TIME:   # the epilogue alone, over the last GEMM's partial sums
         g = lin(x, ws)
         _time(lambda: C().epi_swiglu(g, None, rows // 2, 0, False, 0.0, 0.0, act))
+elif which == "rope_kv":   # QKV projection + RoPE / paged-KV-append epilogue, 70B, 2048-token chunk
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    nq, nkv, d, ps, T, K = 64, 8, 128, 16, 2048, 8192
+    rows = (nq + 2 * nkv) * d
+    lin = QLinear(rand_q4k(rows, K), Q.Q4_K, rows, K, dev)
+    ws = GemmWorkspace(dev, T, rows)
+    x = torch.randn(T, K, device=dev).half()
+    pos = torch.arange(T, dtype=torch.int32, device=dev)
+    inv_freq = 1.0 / (500000.0 ** (torch.arange(0, d, 2, device=dev).float() / d))
+    qo = torch.empty(T, nq, d, device=dev).half()
+    kc = torch.zeros(T // ps, nkv, ps, d, device=dev).half(); vc = torch.zeros_like(kc)
+    run = lambda g: C().epi_rope_kv(g, None, pos, pos, inv_freq, nq, nkv, d, d, False, 1.0, qo,
+                                    kc, vc, ps, None, None, 0.0, None)
+    for _ in range(5):
+        run(lin(x, ws))
+    if TIME:   # the epilogue alone, over the last GEMM's partial sums
+        g = lin(x, ws)
+        _time(lambda: run(g))
+elif which == "delta_decode":  # Qwen3-Next-style recurrent delta rule, decode batch 8, 32 v heads
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    B, nk, nv, D = 8, 16, 32, 128
+    C_ = (2 * nk + nv) * D
+    qkv = torch.randn(B, C_, device=dev)
+    x = torch.randn(B, 2048, device=dev).half()
+    wba = QLinear((torch.randn(2 * nv, 2048, device=dev) * 0.02).half().view(torch.uint8).reshape(-1), Q.F16, 2 * nv, 2048, dev)
+    wz = QLinear((torch.randn(nv * D, 2048, device=dev) * 0.02).half().view(torch.uint8).reshape(-1), Q.F16, nv * D, 2048, dev)
+    gba, gz = wba(x, GemmWorkspace(dev, B, 2 * nv)), wz(x, GemmWorkspace(dev, B, nv * D))
+    A = -torch.rand(nv, device=dev); dtb = torch.rand(nv, device=dev)
+    nw = torch.ones(D, device=dev)
+    state = torch.randn(B + 1, nv, D, D, device=dev) * 0.01     # 16 MB of fp32 state
+    seqs = torch.tensor([[i, 1, i, 100] for i in range(B)], dtype=torch.int32, device=dev)
+    out = torch.zeros(B, nv * D, device=dev).half()
+    run = lambda: C().delta_rule(qkv, nk, nv, D, gba, dtb, A, gz, nw, 1e-6, state, seqs, B, out)
+    for _ in range(5):
+        run()
+    if TIME:
+        _time(run)
 elif which == "tree_rank":  # drafter top-4 over a 128256 vocabulary, 32 sequences x width 4
     rows, V, W = 128, 128256, 4
     logits = torch.randn(rows, V, device=dev) * 3
