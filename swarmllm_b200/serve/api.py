@@ -265,7 +265,7 @@ class Serving:
         v = getattr(self.ae.engine, "vision", None)
         return len(ids) + (len(images) * (v.rows_per_image - 1) if images and v else 0)
 
-    def params(self, body: dict, n_prompt: int) -> SamplingParams:
+    def params(self, body: dict, n_prompt: int, response_format: dict | None = None) -> SamplingParams:
         if body.get("logprobs") or body.get("top_logprobs"):
             # refused rather than ignored, so a client never reads a missing field as "none"
             # (reference behaviour: src/api/openai/mod.rs:298-311)
@@ -280,7 +280,7 @@ class Serving:
             raise ApiError(400, f"prompt ({n_prompt}) + max_tokens ({mt}) exceeds the "
                                 f"context window ({self.max_model_len})")
         t = body.get("temperature")
-        rf = body.get("response_format") or {}
+        rf = response_format or body.get("response_format") or {}
         constraint = None
         if isinstance(rf, dict) and rf.get("type") in ("json_object", "json_schema"):
             from .json_guard import JsonConstraint

@@ -304,7 +304,7 @@ def register(app, S, store_path: str | None = None):
         if fmt and fmt.get("type") == "json_schema":
             fmt = {"type": "json_schema", "json_schema": {"schema": fmt.get("schema")}}
         ids, tools, images = S.prepare(msgs, tools, body.get("tool_choice"), fmt)
-        sp = S.params(body, S.prompt_len(ids, images))
+        sp = S.params(body, S.prompt_len(ids, images), fmt)
         lora = S.lora_of(body)
         persist = body.get("store", True) is not False
         background, stream = bool(body.get("background")), bool(body.get("stream"))

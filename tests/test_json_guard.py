@@ -85,3 +85,22 @@ def test_api_attaches_json_constraint():
             assert c.post("/v1/chat/completions", json=body).status_code == 200
     assert isinstance(seen[0].constraint, JsonConstraint) and seen[1].constraint is None
     ae.shutdown()
+
+
+def test_responses_text_format_attaches_constraint():
+    from test_api_ext import _client
+    c, ae, eng = _client("hi")
+    seen = []
+    orig = eng.add_request
+
+    def spy(ids, sp, request_id, lora=None):
+        seen.append(sp)
+        return orig(ids, sp, request_id, lora)
+    eng.add_request = spy
+    with c:
+        r = c.post("/v1/responses", json={"input": "x", "max_output_tokens": 3,
+                                          "text": {"format": {"type": "json_schema", "name": "s",
+                                                              "schema": {"type": "object"}}}})
+        assert r.status_code == 200, r.text
+    assert isinstance(seen[-1].constraint, JsonConstraint)
+    ae.shutdown()
