@@ -116,24 +116,47 @@ __global__ void __launch_bounds__(kChunkThreads, 1) delta_chunk_kernel(
       sm.G[2 * lane + 1] = excl + g0 + g1;
     }
     __syncthreads();
-    // ---- A (strictly lower) and the masked decayed Q K^T (lower incl. diagonal)
-    for (int e = tid; e < kCh * kCh; e += kChunkThreads) {
-      const int t = e / kCh, u = e % kCh;
-      float av = 0.f, mv = 0.f;
-      if (u <= t) {
-        float dk = 0.f, dq = 0.f;
-#pragma unroll 8
-        for (int i = 0; i < kDk; ++i) {
-          const float ku = sm.k[u][i];
-          dk += sm.k[t][i] * ku;
-          dq += sm.q[t][i] * ku;
+    // ---- A (strictly lower) and the masked decayed Q K^T (lower incl. diagonal):
+    //      a 4 x 4 register tile per thread, rows tb + 16a, columns ub + 16b (with the
+    //      129-float row pitch both operand loads are bank-conflict free)
+    {
+      const int tb = tid >> 4, ub = tid & 15;
+      float dk[4][4], dq[4][4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) dk[x][y] = dq[x][y] = 0.f;
+#pragma unroll 4
+      for (int i = 0; i < kDk; ++i) {
+        float kt[4], qt[4], ku[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          kt[x] = sm.k[tb + 16 * x][i];
+          qt[x] = sm.q[tb + 16 * x][i];
+          ku[x] = sm.k[ub + 16 * x][i];
         }
-        const float dec = __expf(sm.G[t] - sm.G[u]);
-        mv = dec * dq;
-        if (u < t) av = sm.beta[t] * dec * dk;
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+          for (int y = 0; y < 4; ++y) {
+            dk[x][y] += kt[x] * ku[y];
+            dq[x][y] += qt[x] * ku[y];
+          }
       }
-      sm.a[t][u] = av;
-      sm.m[t][u] = mv;
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) {
+          const int t = tb + 16 * x, u = ub + 16 * y;
+          float av = 0.f, mv = 0.f;
+          if (u <= t) {
+            const float dec = __expf(sm.G[t] - sm.G[u]);
+            mv = dec * dq[x][y];
+            if (u < t) av = sm.beta[t] * dec * dk[x][y];
+          }
+          sm.a[t][u] = av;
+          sm.m[t][u] = mv;
+        }
     }
     __syncthreads();
     // ---- forward substitution, one right-hand-side column per thread:
@@ -156,39 +179,100 @@ __global__ void __launch_bounds__(kChunkThreads, 1) delta_chunk_kernel(
       }
     }
     __syncthreads();
-    // ---- D = U - W S0   (in place in u)
+    // ---- D = U - W S0 (in place in u): a 2 x 4 tile per thread, rows tb, tb + 32,
+    //      columns jb + 8c
     {
-      const int j = tid % kDvg;
-      for (int t = tid / kDvg; t < kCh; t += kChunkThreads / kDvg) {
-        float acc = 0.f;
-#pragma unroll 8
-        for (int i = 0; i < kDk; ++i) acc += sm.w[t][i] * sm.s0[i][j];
-        sm.u[t][j] -= acc;
+      const int tb = tid >> 3, jb = tid & 7;
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 4
+      for (int i = 0; i < kDk; ++i) {
+        const float w0 = sm.w[tb][i], w1 = sm.w[tb + 32][i];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float sv = sm.s0[i][jb + 8 * c];
+          acc[0][c] += w0 * sv;
+          acc[1][c] += w1 * sv;
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        sm.u[tb][jb + 8 * c] -= acc[0][c];
+        sm.u[tb + 32][jb + 8 * c] -= acc[1][c];
       }
     }
     __syncthreads();
-    // ---- O = gamma Q S0 + M D   -> o_raw
+    // ---- O = gamma Q S0 + M D -> o_raw (same tiling; M is zero above the diagonal,
+    //      so the u loop runs to the warp's last row)
     {
-      const int j = tid % kDvg;
-      for (int t = tid / kDvg; t < L; t += kChunkThreads / kDvg) {
-        float qs = 0.f, md = 0.f;
-#pragma unroll 8
-        for (int i = 0; i < kDk; ++i) qs += sm.q[t][i] * sm.s0[i][j];
-        for (int u = 0; u <= t; ++u) md += sm.m[t][u] * sm.u[u][j];
-        o_raw[(size_t)(r0 + c0 + t) * nv * kDk + h * kDk + cg * kDvg + j] =
-            __expf(sm.G[t]) * qs + md;
+      const int tb = tid >> 3, jb = tid & 7;
+      const int uend = min(kCh, ((tid >> 5) << 2) + 36);
+      float qs[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      float md[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 4
+      for (int i = 0; i < kDk; ++i) {
+        const float q0 = sm.q[tb][i], q1 = sm.q[tb + 32][i];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float sv = sm.s0[i][jb + 8 * c];
+          qs[0][c] += q0 * sv;
+          qs[1][c] += q1 * sv;
+        }
+      }
+#pragma unroll 4
+      for (int u = 0; u < uend; ++u) {
+        const float m0 = sm.m[tb][u], m1 = sm.m[tb + 32][u];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float dv = sm.u[u][jb + 8 * c];
+          md[0][c] += m0 * dv;
+          md[1][c] += m1 * dv;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int t = tb + 32 * r;
+        if (t < L) {
+          const float gt = __expf(sm.G[t]);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            o_raw[(size_t)(r0 + c0 + t) * nv * kDk + h * kDk + cg * kDvg + jb + 8 * c] =
+                gt * qs[r][c] + md[r][c];
+        }
       }
     }
     __syncthreads();
-    // ---- S0 <- gamma_L S0 + sum_t exp(G_L - G_t) k_t d_t^T   (each entry in place)
+    // ---- S0 <- gamma_L S0 + sum_t exp(G_L - G_t) k_t d_t^T: scale the rows of D by
+    //      exp(G_L - G_t), then a 4 x 4 tile per thread, rows ib + 32a, columns jb + 8c
     {
       const float GL = sm.G[L - 1];
-      const int j = tid % kDvg;
-      for (int i = tid / kDvg; i < kDk; i += kChunkThreads / kDvg) {
-        float acc = __expf(GL) * sm.s0[i][j];
-        for (int t = 0; t < L; ++t) acc += __expf(GL - sm.G[t]) * sm.k[t][i] * sm.u[t][j];
-        sm.s0[i][j] = acc;
+      for (int e = tid; e < kCh * kDvg; e += kChunkThreads) {
+        const int t = e / kDvg, j = e % kDvg;
+        sm.u[t][j] *= __expf(GL - sm.G[t]);
       }
+      __syncthreads();
+      const int ib = tid >> 3, jb = tid & 7;
+      const float gl = __expf(GL);
+      float acc[4][4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[x][c] = gl * sm.s0[ib + 32 * x][jb + 8 * c];
+#pragma unroll 4
+      for (int t = 0; t < L; ++t) {
+        float kv[4], dv[4];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) kv[x] = sm.k[t][ib + 32 * x];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) dv[c] = sm.u[t][jb + 8 * c];
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[x][c] += kv[x] * dv[c];
+      }
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sm.s0[ib + 32 * x][jb + 8 * c] = acc[x][c];
     }
     __syncthreads();
   }

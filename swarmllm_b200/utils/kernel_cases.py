@@ -219,5 +219,8 @@ elif which == "delta":     # Qwen3-Next-style DeltaNet prefill: 4096 tokens, 16 
     oraw = torch.zeros(T, nv * D, device=dev); out = torch.zeros(T, nv * D, device=dev).half()
     for _ in range(3):
         C().delta_chunk(qkv, nk, nv, D, gba, dtb, A, gz, nw, 1e-6, state, seqs, 1, oraw, out)
+    if TIME:
+        _time(lambda: C().delta_chunk(qkv, nk, nv, D, gba, dtb, A, gz, nw, 1e-6, state, seqs, 1,
+                                      oraw, out), n=10)
 torch.cuda.synchronize()
 print("ok", which)

@@ -501,3 +501,39 @@ def test_residual_rmsnorm_rows_path(with_bias):
     ws.check()
     assert rel_err(rd.cpu(), h) < 3e-3
     assert rel_err(out.float().cpu(), ref) < 4e-3
+
+
+def test_delta_chunk_matches_recurrent():
+    """Chunked gated delta rule (prefill) == the token-sequential recurrent
+    kernel on the same inputs: two sequences (one fresh, one resuming a
+    random state), partial last chunks; outputs and final states."""
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    torch.manual_seed(5)
+    nk, nv, D, H = 2, 4, 128, 256
+    seqs_l = [(0, 100, 0, 0), (100, 50, 1, 7)]
+    T = 150
+    C_ = (2 * nk + nv) * D
+    qkv = torch.randn(T, C_, device=DEV)
+    x = (torch.randn(T, H) * 0.5).half().to(DEV)
+    wba = QLinear((torch.randn(2 * nv, H) * 0.05).half().view(torch.uint8).reshape(-1).numpy(),
+                  Q.F16, 2 * nv, H, DEV)
+    wz = QLinear((torch.randn(nv * D, H) * 0.05).half().view(torch.uint8).reshape(-1).numpy(),
+                 Q.F16, nv * D, H, DEV)
+    gba = wba(x, GemmWorkspace(DEV, T, 2 * nv))
+    gz = wz(x, GemmWorkspace(DEV, T, nv * D))
+    A = -torch.rand(nv, device=DEV) * 0.5
+    dtb = torch.rand(nv, device=DEV)
+    nw = (torch.rand(D) + 0.5).to(DEV)
+    st0 = torch.zeros(3, nv, D, D, device=DEV)
+    st0[1] = torch.randn(nv, D, D, device=DEV) * 0.05
+    seqs = torch.tensor(seqs_l, dtype=torch.int32, device=DEV)
+    st_r, st_c = st0.clone(), st0.clone()
+    out_r = torch.zeros(T, nv * D, device=DEV).half()
+    out_c = torch.zeros_like(out_r)
+    oraw = torch.zeros(T, nv * D, device=DEV)
+    C().delta_rule(qkv, nk, nv, D, gba, dtb, A, gz, nw, 1e-6, st_r, seqs, 2, out_r)
+    C().delta_chunk(qkv, nk, nv, D, gba, dtb, A, gz, nw, 1e-6, st_c, seqs, 2, oraw, out_c)
+    torch.cuda.synchronize()
+    assert rel_err(out_c.float().cpu(), out_r.float().cpu()) < 3e-3
+    for slot in (0, 1):
+        assert rel_err(st_c[slot].cpu(), st_r[slot].cpu()) < 1e-3, slot
