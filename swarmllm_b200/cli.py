@@ -182,8 +182,11 @@ def main(argv=None):
         write_random_gguf(preset(args.model), args.out, args.seed)
         print(args.out)
         return
+    from .utils.config import load_logging_settings
     from .utils.logsetup import get_logger, setup_logging
-    setup_logging(args.verbose, args.log_file, args.log_json)
+    lg = load_logging_settings(args.config)
+    setup_logging(args.verbose, args.log_file or lg.get("file"), args.log_json or lg.get("json", False),
+                  level=lg.get("level"))
     eng = _engine(args)
     if args.cmd == "info":
         print(json.dumps({"config": eng.cfg.to_dict(), "kv_pages": eng.bm.num_pages,

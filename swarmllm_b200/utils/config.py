@@ -17,6 +17,10 @@ SWARMLLM_KV_PAGES, SWARMLLM_KV_FRACTION, SWARMLLM_PREFIX_CACHE, SWARMLLM_CUDA_GR
 
 A [server] table (rpm, cors_origins, max_body) holds the request-guard
 settings; the admin API re-reads it on /api/admin/config/reload.
+
+A [logging] table (the reference's names: level = trace|debug|info|warn|error,
+format = pretty|json; plus file = a rotating log file) sets up logging when
+the command line does not.
 """
 from __future__ import annotations
 
@@ -66,6 +70,23 @@ def load_engine_config(path: str | None = None, env=None) -> EngineConfig:
     if cfg.max_step_tokens < cfg.prefill_chunk:
         cfg.max_step_tokens = cfg.prefill_chunk
     return cfg
+
+
+def load_logging_settings(path: str | None) -> dict:
+    """level / format / file from a TOML [logging] table ({} without one)."""
+    if not path:
+        return {}
+    import tomllib
+    with open(path, "rb") as f:
+        lg = tomllib.load(f).get("logging", {})
+    out = {}
+    if lg.get("level") in ("trace", "debug", "info", "warn", "warning", "error"):
+        out["level"] = lg["level"]
+    if lg.get("format") in ("pretty", "json"):
+        out["json"] = lg["format"] == "json"
+    if isinstance(lg.get("file"), str) and lg["file"]:
+        out["file"] = lg["file"]
+    return out
 
 
 def load_server_settings(path: str) -> dict:

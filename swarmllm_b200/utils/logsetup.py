@@ -25,11 +25,17 @@ class JsonFormatter(logging.Formatter):
         return json.dumps(d)
 
 
+_LEVELS = {"trace": logging.DEBUG, "debug": logging.DEBUG, "info": logging.INFO,
+           "warn": logging.WARNING, "warning": logging.WARNING, "error": logging.ERROR}
+
+
 def setup_logging(verbosity: int = 0, log_file: str | None = None, json_format: bool = False,
-                  max_bytes: int = 50 << 20, backups: int = 3) -> logging.Logger:
-    """verbosity 0: info, 1+: debug.  Idempotent: replaces this logger's handlers."""
+                  max_bytes: int = 50 << 20, backups: int = 3,
+                  level: str | None = None) -> logging.Logger:
+    """verbosity 0: info (or `level`), 1+: debug.  Idempotent: replaces this
+    logger's handlers."""
     log = logging.getLogger(LOGGER)
-    log.setLevel(logging.DEBUG if verbosity > 0 else logging.INFO)
+    log.setLevel(logging.DEBUG if verbosity > 0 else _LEVELS.get(level or "info", logging.INFO))
     for h in list(log.handlers):
         log.removeHandler(h)
         h.close()

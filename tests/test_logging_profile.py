@@ -34,3 +34,16 @@ def test_stage_profiler_accounts_named_stages():
     with off.stage("x"):
         pass
     assert off.counts == {}
+
+
+def test_logging_settings_from_toml(tmp_path):
+    from swarmllm_b200.utils.config import load_logging_settings
+    from swarmllm_b200.utils.logsetup import setup_logging
+    p = tmp_path / "c.toml"
+    p.write_text('[logging]\nlevel = "warn"\nformat = "json"\nfile = "%s"\n' % (tmp_path / "x.log"))
+    lg = load_logging_settings(str(p))
+    assert lg == {"level": "warn", "json": True, "file": str(tmp_path / "x.log")}
+    log = setup_logging(0, lg["file"], lg["json"], level=lg["level"])
+    assert log.level == logging.WARNING
+    assert load_logging_settings(None) == {}
+    setup_logging(0)
