@@ -205,15 +205,41 @@ class LLMEngine:
             adapter = LoraAdapter.from_gguf(adapter, name)
         if name:
             adapter.name = name
+        if adapter.name in self.lora_names:
+            return adapter.name
         if getattr(self.model, "lora", None) is not None:
-            self.model.lora.add(adapter)
+            slot = self.model.lora.add(adapter)
         elif hasattr(self.model, "lora_adapters"):
-            self.model.lora_adapters.append(adapter)
+            ads = self.model.lora_adapters
+            slot = ads.index(None) if None in ads else len(ads)
+            if slot == len(ads):
+                ads.append(adapter)
+            else:
+                ads[slot] = adapter
         else:
             raise RuntimeError("engine built without LoRA slots (EngineConfig.max_loras)")
-        if adapter.name not in self.lora_names:
-            self.lora_names.append(adapter.name)
+        # a request's adapter id is its slot: the name list mirrors the slots
+        while len(self.lora_names) <= slot:
+            self.lora_names.append(None)
+        self.lora_names[slot] = adapter.name
         return adapter.name
+
+    def unload_lora(self, name: str) -> int:
+        """Free an adapter's slot; refused while a live request uses it."""
+        if name not in self.lora_names:
+            raise KeyError(name)
+        slot = self.lora_names.index(name)
+        if slot in self.lora_of.values():
+            raise RuntimeError(f"adapter {name!r} is in use by a running request")
+        if getattr(self.model, "lora", None) is not None:
+            self.model.lora.remove(name)
+        else:
+            self.model.lora_adapters[slot] = None
+        self.lora_names[slot] = None
+        return slot
+
+    def adapters(self) -> list[str]:
+        return [n for n in self.lora_names if n is not None]
 
     def load_vision(self, mmproj_path: str):
         """Image encoder for prompts with images (an mmproj GGUF)."""

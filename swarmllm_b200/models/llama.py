@@ -609,7 +609,7 @@ class LlamaCPU:
         base = f"blk.{layer}.{suffix}.weight"
         ids = b.lora_ids.long()
         for a, ad in enumerate(ads):
-            if base not in ad.tensors:
+            if ad is None or base not in ad.tensors:   # a freed slot
                 continue
             rows = (ids == a).nonzero().flatten()
             if len(rows) == 0:

@@ -115,12 +115,22 @@ class LoraSet:
     def index(self, name: str) -> int:
         return self.names.index(name)
 
+    def remove(self, name: str) -> int:
+        """Free an adapter's slot (its tables zeroed); returns the slot."""
+        a = self.names.index(name)
+        for At, Bt, S, _ in self.tables.values():
+            At[a].zero_()
+            Bt[a].zero_()
+            S[a] = 1.0
+        self.names[a] = None
+        return a
+
     def add(self, ad: LoraAdapter) -> int:
         if ad.name in self.names:
             return self.names.index(ad.name)
-        if len(self.names) >= self.M:
+        a = self.names.index(None) if None in self.names else len(self.names)
+        if a >= self.M:
             raise ValueError(f"at most {self.M} adapters")
-        a = len(self.names)
         cfg, m = self.model.cfg, self.model
         d = cfg.head_dim
         qh = 2 * d if cfg.attn_output_gate else d
@@ -142,5 +152,8 @@ class LoraSet:
                 At[a, off:off + r] = torch.from_numpy(A_).to(At.device, torch.float16)
                 Bt[a, r0:r0 + B_.shape[0], off:off + r] = torch.from_numpy(
                     B_ * ad.scale(base)).to(Bt.device, torch.float16)
-        self.names.append(ad.name)
+        if a == len(self.names):
+            self.names.append(ad.name)
+        else:
+            self.names[a] = ad.name
         return a

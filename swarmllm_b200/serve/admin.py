@@ -14,7 +14,15 @@
   GET  /api/admin/diagnostics    devices (memory, SMs, clocks), software
                                  versions, native extensions loaded, KV cache
   GET  /api/admin/responses      stored /v1/responses ids (newest first)
-  GET  /api/admin/storage        the model's files and their sizes
+  GET  /api/admin/storage        the model's files and their sizes (also /storage/breakdown)
+  GET  /api/admin/adapters       LoRA adapters and their slots; POST loads one
+  DELETE /api/admin/adapters/{id}  unload one (409 while a request uses it)
+  GET  /api/admin/models/{id}    one served model (base or adapter); /status: loaded, ready
+  GET  /api/admin/version        package and library versions
+  GET  /api/admin/peers          none on one node (the GPUs are ranks, not peers)
+  GET  /api/admin/schedule       scheduler state: running, waiting, preemptions, limits
+  GET  /api/admin/swarm/capacity free KV tokens, GPUs, concurrency limits
+  POST /api/admin/shutdown       graceful stop of a server started by serve()
 
 Every route needs the API key when one is configured (the guards treat
 /api/admin like any other path).  Model download and Hugging Face search are
@@ -116,7 +124,7 @@ def register(app, S, settings, config_path: str | None = None):
         v = getattr(e, "vision", None)
         return {"model": cfg.name, "arch": cfg.arch, "layers": cfg.n_layers, "hidden": cfg.hidden,
                 "vocab": cfg.vocab, "params": cfg.param_count(), "linear_weight_bytes": weight_bytes,
-                "linear_types": types, "lora_adapters": list(getattr(e, "lora_names", [])),
+                "linear_types": types, "lora_adapters": [n for n in getattr(e, "lora_names", []) if n],
                 "lora_slots": e.ecfg.max_loras,
                 "vision": None if v is None else {"projector": v.cfg.projector,
                                                   "image_size": v.cfg.image_size,
@@ -137,6 +145,83 @@ def register(app, S, settings, config_path: str | None = None):
             raise ApiError(400, str(ex))
         return {"loaded": n, "models": S.models()}
 
+    @app.get("/api/admin/adapters")
+    async def adapters():
+        e = engine()
+        return {"data": [{"id": n, "slot": i, "model": f"{S.model_name}:{n}"}
+                         for i, n in enumerate(getattr(e, "lora_names", [])) if n],
+                "slots": e.ecfg.max_loras}
+
+    @app.post("/api/admin/adapters")
+    async def add_adapter(request: Request):
+        return await load_lora(request)
+
+    @app.delete("/api/admin/adapters/{name}")
+    async def remove_adapter(name: str):
+        try:
+            slot = await S.ae.call(lambda e: e.unload_lora(name))
+        except KeyError:
+            raise ApiError(404, f"no adapter {name!r}")
+        except RuntimeError as ex:
+            raise ApiError(409, str(ex))
+        return {"removed": name, "slot": slot, "models": S.models()}
+
+    @app.get("/api/admin/models/{mid}")
+    async def model_detail(mid: str):
+        if mid not in S.models() and S.lora_of({"model": mid}) is None:
+            raise ApiError(404, f"no model {mid!r}")
+        d = await models()
+        d["id"] = mid
+        d["adapter"] = S.lora_of({"model": mid})
+        return d
+
+    @app.get("/api/admin/models/{mid}/status")
+    async def model_status(mid: str):
+        if mid not in S.models() and S.lora_of({"model": mid}) is None:
+            raise ApiError(404, f"no model {mid!r}")
+        return {"id": mid, "loaded": True, "ready": S.ae.ready}
+
+    @app.get("/api/admin/version")
+    async def version():
+        import torch
+
+        from .. import __version__
+        return {"name": "swarmllm_b200", "version": __version__, "torch": torch.__version__,
+                "cuda": torch.version.cuda}
+
+    @app.get("/api/admin/peers")
+    async def peers():
+        # one node: the GPUs are ranks of this process group, not swarm peers
+        return {"peers": [], "node": {"model": S.model_name, "ready": S.ae.ready}}
+
+    @app.get("/api/admin/schedule")
+    async def schedule():
+        e = engine()
+        ec = e.ecfg
+        return {"running": e.sched.num_running, "waiting": e.sched.num_waiting,
+                "preemptions": getattr(e.sched, "num_preemptions", 0), "steps": e.steps,
+                "max_running": ec.max_running, "max_step_tokens": ec.max_step_tokens,
+                "prefill_chunk": ec.prefill_chunk, "kv_pages_free": e.bm.num_free(),
+                "kv_pages": e.bm.num_pages, "page_size": e.bm.page_size}
+
+    @app.get("/api/admin/swarm/capacity")
+    async def capacity():
+        e = engine()
+        import torch
+        return {"gpus": torch.cuda.device_count() if torch.cuda.is_available() else 0,
+                "kv_tokens_free": e.bm.num_free() * e.bm.page_size,
+                "kv_tokens": e.bm.num_pages * e.bm.page_size,
+                "running": e.sched.num_running, "max_running": e.ecfg.max_running,
+                "max_model_len": e.ecfg.max_model_len}
+
+    @app.post("/api/admin/shutdown")
+    async def shutdown():
+        hook = getattr(app.state, "shutdown_hook", None)
+        if hook is None:
+            raise ApiError(501, "this server was not started by serve(): no shutdown hook")
+        hook()
+        return {"status": "shutting down"}
+
     @app.get("/api/admin/diagnostics")
     async def diagnostics():
         from ..utils.diagnostics import collect
@@ -152,6 +237,7 @@ def register(app, S, settings, config_path: str | None = None):
                                     (max(1, min(1000, int(limit))),)).fetchall()
         return {"data": [{"id": r[0], "created": r[1]} for r in rows]}
 
+    @app.get("/api/admin/storage/breakdown")
     @app.get("/api/admin/storage")
     async def storage():
         src = getattr(engine(), "source_path", None)

@@ -258,7 +258,7 @@ class Serving:
 
     def models(self) -> list[str]:
         return [self.model_name] + [f"{self.model_name}:{n}" for n in
-                                    getattr(self.ae.engine, "lora_names", None) or []]
+                                    getattr(self.ae.engine, "lora_names", None) or [] if n]
 
     def prompt_len(self, ids, images) -> int:
         """Positions the prompt takes once each image marker is its rows."""
@@ -762,7 +762,9 @@ def serve(engine, tokenizer, model_name: str, host: str = "0.0.0.0", port: int =
     import uvicorn
     ae = AsyncEngine(engine)
     app = create_app(ae, tokenizer, model_name, port=port, **kw)
+    server = uvicorn.Server(uvicorn.Config(app, host=host, port=port, log_level="info"))
+    app.state.shutdown_hook = lambda: setattr(server, "should_exit", True)   # admin shutdown
     try:
-        uvicorn.run(app, host=host, port=port, log_level="info")
+        server.run()
     finally:
         ae.shutdown()

@@ -392,6 +392,33 @@ def test_admin_api(tmp_path):
         d = c.get("/api/admin/diagnostics", headers=h).json()
         assert d["native_extensions"]["swarmllm_b200._native"] and d["kv_cache"]["pages"] > 0
         assert c.get("/api/admin/responses", headers=h).json()["data"] == []
+        ad = c.get("/api/admin/adapters", headers=h).json()
+        assert ad["data"][0]["id"] == "ad" and ad["slots"] == 1
+        assert c.get("/api/admin/models/tiny:ad", headers=h).json()["adapter"] == "ad"
+        assert c.get("/api/admin/models/tiny/status", headers=h).json()["ready"] is True
+        assert c.get("/api/admin/models/nope/status", headers=h).status_code == 404
+        assert c.get("/api/admin/version", headers=h).json()["name"] == "swarmllm_b200"
+        assert c.get("/api/admin/peers", headers=h).json()["peers"] == []
+        assert c.get("/api/admin/schedule", headers=h).json()["max_running"] == 4
+        assert c.get("/api/admin/swarm/capacity", headers=h).json()["kv_tokens"] > 0
+        assert c.get("/api/admin/storage/breakdown", headers=h).status_code == 200
+        assert c.post("/api/admin/shutdown", headers=h).status_code == 501    # no hook here
+        # unload; the freed slot is reused by the next load
+        r = c.delete("/api/admin/adapters/ad", headers=h)
+        assert r.status_code == 200 and "tiny:ad" not in r.json()["models"]
+        assert c.delete("/api/admin/adapters/ad", headers=h).status_code == 404
+        assert c.post("/api/admin/adapters", json={"name": "ad2", "path": p}, headers=h).status_code == 200
+        assert c.get("/api/admin/adapters", headers=h).json()["data"] == [
+            {"id": "ad2", "slot": 0, "model": "tiny:ad2"}]
+        r = c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 2, "model": "tiny:ad2"},
+                   headers=h)
+        assert r.status_code == 200
+        called = []
+        app.state.shutdown_hook = lambda: called.append(1)
+        assert c.post("/api/admin/shutdown", headers=h).status_code == 200 and called
+    eng.lora_of[999] = 0                       # a live request on the adapter's slot
+    with pytest.raises(RuntimeError):
+        eng.unload_lora("ad2")
     ae.shutdown()
 
 

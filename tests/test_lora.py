@@ -163,3 +163,33 @@ def test_gpu_engine_lora_graphs_and_mixed_batch():
     base = LLMEngine.from_config(cfg, DEV, ec, source=RandomSource(cfg, seed=5)).generate(prompts, sp)
     assert res[1][0] == base[0].token_ids and res[1][3] == base[3].token_ids
     assert res[1][1] != base[1].token_ids
+
+
+@pytest.mark.gpu
+def test_gpu_lora_unload_frees_slot():
+    """Unloading an adapter zeroes its slot; the next adapter loaded there gives
+    the same tokens as an engine that only ever held that adapter."""
+    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from swarmllm_b200.models.lora import LoraAdapter
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = _cfg("Q4_K")
+    prompt = np.random.default_rng(3).integers(0, cfg.vocab, 21).tolist()
+    sp = SamplingParams(max_tokens=8)
+    ec = EngineConfig(max_model_len=128, max_running=4, max_step_tokens=128, prefill_chunk=64,
+                      graph_sizes=(1, 2, 4), max_loras=1, max_lora_rank=8)
+
+    def run(eng, name):
+        rid = eng.add_request(prompt, sp, lora=name)
+        out = []
+        while eng.has_work():
+            out += [t for r, t, _ in eng.step() if r == rid]
+        return out
+    eng = LLMEngine.from_config(cfg, DEV, ec, source=RandomSource(cfg, seed=5))
+    eng.load_lora(LoraAdapter.random(cfg, rank=8, seed=31, std=0.3), "a")
+    run(eng, "a")
+    assert eng.unload_lora("a") == 0
+    eng.load_lora(LoraAdapter.random(cfg, rank=4, seed=32, std=0.3, targets=("attn_q", "ffn_down")), "b")
+    got = run(eng, "b")
+    ref_eng = LLMEngine.from_config(cfg, DEV, ec, source=RandomSource(cfg, seed=5))
+    ref_eng.load_lora(LoraAdapter.random(cfg, rank=4, seed=32, std=0.3, targets=("attn_q", "ffn_down")), "b")
+    assert got == run(ref_eng, "b")
