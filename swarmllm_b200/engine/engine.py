@@ -18,7 +18,7 @@ import dataclasses
 import hashlib
 import itertools
 import time
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 import torch

@@ -3,7 +3,6 @@
 layer 1 across 2 local processes over gloo; 4 prompts of 32 random ids,
 greedy decode of 64 tokens; logits must match a single-process run."""
 import os
-import tempfile
 
 import numpy as np
 import pytest
