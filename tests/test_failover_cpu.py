@@ -57,7 +57,10 @@ def _worker(rank, world, port, ctl_port, crash_rank, crash_after, q):
             eng.step = step
         return eng
 
-    rp = ResilientPipeline(build, rank, world, "127.0.0.1", ctl_port, pg_timeout_s=5.0)
+    # grace well above the group timeout: a survivor that learns of the failure
+    # only from its own 5 s timeout must still register on a loaded machine
+    rp = ResilientPipeline(build, rank, world, "127.0.0.1", ctl_port, pg_timeout_s=5.0,
+                           grace_s=15.0)
     out = rp.generate(_prompts(), SamplingParams(max_tokens=10, ignore_eos=True))
     if rank == 0:
         q.put((out, rp.recoveries, rp.members))
