@@ -139,7 +139,7 @@ __global__ void epi_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ resid
 // Layout of the QKV GEMM rows: [q heads][k heads][v heads], each head_dim
 // wide -- or, for gated attention, each q head as [q | gate].
 // Cache layout: [pages][n_kv][page_size][head_dim] fp16.
-constexpr int kRopeHpb = 4;
+constexpr int kRopeHpb = 8;
 
 __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
                                    const int32_t* __restrict__ positions,
@@ -212,6 +212,51 @@ __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
     __syncthreads();
   }
   const int half = rope_dim / 2, hd2 = head_dim / 2;
+  if ((half & 1) == 0 && (rope_dim & 3) == 0 && (head_dim & 3) == 0 &&
+      ((reinterpret_cast<uintptr_t>(q_out) | reinterpret_cast<uintptr_t>(k_cache)) & 7) == 0) {
+    // Two adjacent dimension pairs per thread (pair index p even): the rotated
+    // halves go out as 4-byte stores (NEOX: p, p + 1 and p + half, p + half + 1)
+    // or one 8-byte store (interleaved pairs, and the unrotated tail).
+    const int hq = hd2 >> 1;
+    for (int i = threadIdx.x; i < nh * hq; i += blockDim.x) {
+      const int j = i / hq, p = 2 * (i - j * hq);
+      const int hh = h0 + j;
+      if (hh >= n_q + n_kv) continue;
+      __half* dst;
+      if (hh < n_q) {
+        dst = q_out + ((size_t)t * n_q + hh) * head_dim;
+      } else if (slot >= 0) {
+        dst = k_cache + (((size_t)page * n_kv + (hh - n_q)) * page_size + off) * head_dim;
+      } else {
+        continue;
+      }
+      const float* x = sh + j * head_dim;
+      if (p < half) {   // both pairs rotated (half is even)
+        float s0, c0, s1, c1;
+        sincosf((float)pos * inv_freq[p], &s0, &c0);
+        sincosf((float)pos * inv_freq[p + 1], &s1, &c1);
+        c0 *= attn_factor; s0 *= attn_factor; c1 *= attn_factor; s1 *= attn_factor;
+        if (neox) {
+          const float a0 = x[p], a1 = x[p + 1], b0 = x[p + half], b1 = x[p + 1 + half];
+          *reinterpret_cast<__half2*>(dst + p) =
+              __floats2half2_rn(a0 * c0 - b0 * s0, a1 * c1 - b1 * s1);
+          *reinterpret_cast<__half2*>(dst + p + half) =
+              __floats2half2_rn(b0 * c0 + a0 * s0, b1 * c1 + a1 * s1);
+        } else {
+          const float a0 = x[2 * p], b0 = x[2 * p + 1], a1 = x[2 * p + 2], b1 = x[2 * p + 3];
+          __align__(8) __half2 y[2] = {__floats2half2_rn(a0 * c0 - b0 * s0, b0 * c0 + a0 * s0),
+                                       __floats2half2_rn(a1 * c1 - b1 * s1, b1 * c1 + a1 * s1)};
+          *reinterpret_cast<uint2*>(dst + 2 * p) = *reinterpret_cast<const uint2*>(y);
+        }
+      } else {          // both pairs in the unrotated tail: four contiguous values
+        const int d0 = rope_dim + 2 * (p - half);
+        __align__(8) __half2 y[2] = {__floats2half2_rn(x[d0], x[d0 + 1]),
+                                     __floats2half2_rn(x[d0 + 2], x[d0 + 3])};
+        *reinterpret_cast<uint2*>(dst + d0) = *reinterpret_cast<const uint2*>(y);
+      }
+    }
+    return;
+  }
   // One thread per dimension pair: rotated pairs share one sincos; the
   // unrotated tail (partial RoPE) is copied pairwise.
   for (int i = threadIdx.x; i < nh * hd2; i += blockDim.x) {
@@ -457,7 +502,7 @@ void launch_epi_rope_kv(const GemmOut& g, const float* bias, const int32_t* posi
   if (g.T <= 0) return;
   const size_t sm = (size_t)kRopeHpb * head_dim * sizeof(float);
   const int groups = (n_q + 2 * n_kv + kRopeHpb - 1) / kRopeHpb;
-  epi_rope_kv_kernel<<<dim3(g.T, groups), 128, sm, s>>>(
+  epi_rope_kv_kernel<<<dim3(g.T, groups), 256, sm, s>>>(
       g, bias, positions, slots, inv_freq, n_q, n_kv, head_dim, rope_dim, neox, attn_factor,
       q_out, k_cache, v_cache, page_size, q_norm_w, k_norm_w, norm_eps, gate_out);
   SW_LAUNCH_CHECK();

@@ -185,9 +185,12 @@ def test_epi_residual_rmsnorm():
     assert rel_err(out.float().cpu(), ref) < 2e-3
 
 
-@pytest.mark.parametrize("neox,rope_dim", [(False, 64), (True, 64), (True, 32)])
-def test_epi_rope_kv(neox, rope_dim):
-    T, nq, nkv, d, ps = 6, 4, 2, 64, 16
+# rope_dim 34 (odd half) takes the one-pair-per-thread path, the others the
+# two-pairs-per-thread vector path; nq 6 leaves a partial 8-head group
+@pytest.mark.parametrize("neox,rope_dim,nq", [(False, 64, 4), (True, 64, 4), (True, 32, 4),
+                                              (False, 48, 6), (True, 34, 4), (False, 34, 6)])
+def test_epi_rope_kv(neox, rope_dim, nq):
+    T, nkv, d, ps = 6, 2, 64, 16
     R = (nq + 2 * nkv) * d
     g, v = _gemm_identity(torch.randn(T, R))
     pos = torch.tensor([0, 3, 17, 100, 4095, 9], dtype=torch.int32)
