@@ -183,6 +183,7 @@ def test_gpu_lora_unload_frees_slot():
         out = []
         while eng.has_work():
             out += [t for r, t, _ in eng.step() if r == rid]
+        eng.release(rid)        # a finished request keeps its adapter until released
         return out
     eng = LLMEngine.from_config(cfg, DEV, ec, source=RandomSource(cfg, seed=5))
     eng.load_lora(LoraAdapter.random(cfg, rank=8, seed=31, std=0.3), "a")
