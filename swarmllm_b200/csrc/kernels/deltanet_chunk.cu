@@ -90,17 +90,19 @@ __global__ void __launch_bounds__(kChunkThreads, 1) delta_chunk_kernel(
         sm.k[t][lane + 32 * e] = kv[e] * ik;
       }
       sm.v[t][lane] = valid ? xr[2 * nk * kDk + h * kDk + cg * kDvg + lane] : 0.f;
-      if (lane == 0) {
-        float b = 0.f, gdec = 0.f;
-        if (valid) {
-          const int row = r0 + c0 + t;
-          const float bl = gba.get(row, h), al = gba.get(row, nv + h) + dtb;
-          b = 1.f / (1.f + __expf(-bl));
-          gdec = Ah * (al > 20.f ? al : log1pf(__expf(al)));
-        }
-        sm.beta[t] = b;
-        sm.G[t] = gdec;
+    }
+    // gates: one row per thread, so the 64 rows' partial-sum reads are in flight together
+    if (tid < kCh) {
+      const int t = tid;
+      float b = 0.f, gdec = 0.f;
+      if (t < L) {
+        const int row = r0 + c0 + t;
+        const float bl = gba.get(row, h), al = gba.get(row, nv + h) + dtb;
+        b = 1.f / (1.f + __expf(-bl));
+        gdec = Ah * (al > 20.f ? al : log1pf(__expf(al)));
       }
+      sm.beta[t] = b;
+      sm.G[t] = gdec;
     }
     __syncthreads();
     if (warp == 0) {  // inclusive prefix sum of the log decays (64 values, 2 per lane)
