@@ -26,6 +26,8 @@ class SamplingParams:
     ignore_eos: bool = False
     frequency_penalty: float = 0.0   # per occurrence in the completion so far
     presence_penalty: float = 0.0    # once for any token the completion contains
+    # token id -> value added to its logit before sampling (OpenAI logit_bias)
+    logit_bias: dict = field(default=None, compare=False, repr=False)
     # per-request token filter applied before a token is committed (serve/json_guard.py):
     # .choose(drawn, candidates) -> token or None, .accept(token)
     constraint: object = field(default=None, compare=False, repr=False)
@@ -36,25 +38,35 @@ class SamplingParams:
 
     @property
     def penalized(self) -> bool:
-        return self.frequency_penalty != 0.0 or self.presence_penalty != 0.0
+        """The logits are adjusted before sampling (penalties or logit bias)."""
+        return self.frequency_penalty != 0.0 or self.presence_penalty != 0.0 or bool(self.logit_bias)
 
 
 def penalty_table(params: list[SamplingParams], history: list | None):
     """CSR table (row offsets int32 [S + 1], tokens int32, values f32) of the
-    logit penalties of each sampled row: for every distinct token t the
-    request generated so far (the prompt excluded), count(t) *
-    frequency_penalty + presence_penalty, subtracted from the raw logit before
-    temperature.  None when no row is penalized.
+    logit adjustments of each sampled row, subtracted from the raw logits
+    before temperature: for every distinct token t the request generated so
+    far (the prompt excluded), count(t) * frequency_penalty +
+    presence_penalty; minus the request's logit_bias for t.  None when no row
+    is adjusted.
     Reference behaviour: src/inference/sampling.rs:75-125."""
-    if history is None or not any(p.penalized for p in params):
+    if not any(p.penalized for p in params):
         return None
+    if history is None:
+        history = [None] * len(params)
     off, tok, val = [0], [], []
     for p, h in zip(params, history):
-        if p.penalized and h:
+        row: dict = {}
+        if h and (p.frequency_penalty != 0.0 or p.presence_penalty != 0.0):
             for t, c in h.items():
-                tok.append(int(t))
-                val.append(c * p.frequency_penalty + p.presence_penalty)
+                row[int(t)] = c * p.frequency_penalty + p.presence_penalty
+        for t, b in (p.logit_bias or {}).items():     # a bias adds: subtract its negative
+            row[int(t)] = row.get(int(t), 0.0) - float(b)
+        tok.extend(row.keys())
+        val.extend(row.values())
         off.append(len(tok))
+    if not tok:      # nothing to adjust (no history yet, no bias)
+        return None
     return (np.asarray(off, np.int32), np.asarray(tok, np.int32), np.asarray(val, np.float32))
 
 

@@ -30,6 +30,7 @@ across HTTP requests automatically.
 from __future__ import annotations
 
 import asyncio
+import dataclasses
 import itertools
 import os
 import json
@@ -285,8 +286,17 @@ class Serving:
         if isinstance(rf, dict) and rf.get("type") in ("json_object", "json_schema"):
             from .json_guard import JsonConstraint
             constraint = JsonConstraint(self.piece, int(self.eos))
+        bias = None
+        lb = body.get("logit_bias")
+        if lb:
+            if not isinstance(lb, dict):
+                raise ApiError(400, "logit_bias must map token ids to numbers")
+            try:
+                bias = {int(k): max(-100.0, min(100.0, float(v))) for k, v in lb.items()}
+            except (TypeError, ValueError):
+                raise ApiError(400, "logit_bias must map token ids to numbers")
         return SamplingParams(max_tokens=int(mt), temperature=float(1.0 if t is None else t),
-                              constraint=constraint,
+                              constraint=constraint, logit_bias=bias,
                               top_p=float(body.get("top_p", 1.0) or 1.0),
                               top_k=int(body.get("top_k", 0) or 0),
                               seed=int(body.get("seed", 0) or 0), eos_token_id=int(self.eos),
@@ -300,6 +310,30 @@ class Serving:
         if p is None:
             p = self._pieces[tok] = self.tok.decode([tok])
         return p
+
+    MAX_N = 16
+
+    def n_of(self, body: dict) -> int:
+        """How many independent choices a request asks for (OpenAI `n`)."""
+        n = body.get("n", 1)
+        if n is None:
+            return 1
+        if not isinstance(n, int) or isinstance(n, bool) or not 1 <= n <= self.MAX_N:
+            raise ApiError(400, f"n must be an integer from 1 to {self.MAX_N}")
+        if n > 1 and body.get("stream"):
+            raise ApiError(400, "n > 1 is served without streaming only; set stream to false")
+        return n
+
+    @staticmethod
+    def variants(sp: SamplingParams, n: int) -> list[SamplingParams]:
+        """n request parameter sets: their own constraint state, and when
+        sampling, consecutive seeds so the choices differ."""
+        out = []
+        for i in range(n):
+            seed = sp.seed + i if sp.temperature > 0 else sp.seed
+            c = sp.constraint.fresh() if (sp.constraint is not None and i) else sp.constraint
+            out.append(dataclasses.replace(sp, seed=seed, constraint=c))
+        return out
 
     @staticmethod
     def stops(body: dict) -> list[str]:
@@ -515,6 +549,7 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
             raise ApiError(400, str(e))
         ids, tools, images = S.prepare(msgs, tools, body.get("tool_choice"), body.get("response_format"))
         sp = S.params(body, S.prompt_len(ids, images))
+        n = S.n_of(body)
         lora = S.lora_of(body)
         stops = S.stops(body)
         cid = "chatcmpl-" + uuid.uuid4().hex[:24]
@@ -546,15 +581,20 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
                                              "total_tokens": r.n_prompt + r.n_out}})
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
-        r = await S.run(ids, sp, stops, tools, lora, images)
-        msg = {"role": "assistant", "content": r.text if (r.text or not r.calls) else None}
-        if r.calls:
-            msg["tool_calls"] = [c.openai() for c in r.calls]
+        rs = await asyncio.gather(*[S.run(ids, v, stops, tools, lora, images)
+                                    for v in S.variants(sp, n)])
+        choices = []
+        for i, r in enumerate(rs):
+            msg = {"role": "assistant", "content": r.text if (r.text or not r.calls) else None}
+            if r.calls:
+                msg["tool_calls"] = [c.openai() for c in r.calls]
+            choices.append({"index": i, "message": msg, "finish_reason": r.finish})
+        n_out = sum(r.n_out for r in rs)
         return JSONResponse({
             "id": cid, "object": "chat.completion", "created": created, "model": model,
-            "choices": [{"index": 0, "message": msg, "finish_reason": r.finish}],
-            "usage": {"prompt_tokens": r.n_prompt, "completion_tokens": r.n_out,
-                      "total_tokens": r.n_prompt + r.n_out}}, headers=headers_of(r.trace))
+            "choices": choices,
+            "usage": {"prompt_tokens": rs[0].n_prompt, "completion_tokens": n_out,
+                      "total_tokens": rs[0].n_prompt + n_out}}, headers=headers_of(rs[0].trace))
 
     # ------------------------------------------------------------------ OpenAI completions
     @app.post("/v1/completions")
@@ -564,6 +604,7 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
         ids = list(p) if isinstance(p, list) and p and isinstance(p[0], int) else tokenizer.encode(
             p if isinstance(p, str) else "".join(p))
         sp = S.params(body, len(ids))
+        n = S.n_of(body)
         lora = S.lora_of(body)
         cid = "cmpl-" + uuid.uuid4().hex[:24]
         if body.get("stream"):
@@ -578,11 +619,14 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
                     yield sse(ch)
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
-        r = await S.run(ids, sp, S.stops(body), None, lora)
+        rs = await asyncio.gather(*[S.run(ids, v, S.stops(body), None, lora)
+                                    for v in S.variants(sp, n)])
+        n_out = sum(r.n_out for r in rs)
         return {"id": cid, "object": "text_completion", "model": model_name,
-                "choices": [{"index": 0, "text": r.text, "finish_reason": r.finish}],
-                "usage": {"prompt_tokens": r.n_prompt, "completion_tokens": r.n_out,
-                          "total_tokens": r.n_prompt + r.n_out}}
+                "choices": [{"index": i, "text": r.text, "finish_reason": r.finish}
+                            for i, r in enumerate(rs)],
+                "usage": {"prompt_tokens": rs[0].n_prompt, "completion_tokens": n_out,
+                          "total_tokens": rs[0].n_prompt + n_out}}
 
     # ------------------------------------------------------------------ Anthropic messages
     @app.post("/v1/messages")

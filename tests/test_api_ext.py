@@ -487,3 +487,33 @@ def test_logprobs_refused_not_ignored():
                                                  "logprobs": False, "max_tokens": 2})
         assert r.status_code == 200
     ae.shutdown()
+
+
+def test_n_choices_and_logit_bias_parameters():
+    c, ae, eng = _client("hey")
+    seen = []
+    orig = eng.add_request
+
+    def spy(ids, sp, request_id, lora=None):
+        seen.append(sp)
+        return orig(ids, sp, request_id, lora)
+    eng.add_request = spy
+    msgs = [{"role": "user", "content": "x"}]
+    with c:
+        r = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 8, "n": 3,
+                                                 "temperature": 0.7, "seed": 10})
+        j = r.json()
+        assert r.status_code == 200 and [ch["index"] for ch in j["choices"]] == [0, 1, 2]
+        assert all(ch["message"]["content"] == "hey" for ch in j["choices"])
+        assert sorted(sp.seed for sp in seen[-3:]) == [10, 11, 12]
+        assert j["usage"]["completion_tokens"] == 3 * 4
+        r = c.post("/v1/completions", json={"prompt": "x", "max_tokens": 8, "n": 2})
+        assert [ch["index"] for ch in r.json()["choices"]] == [0, 1]
+        assert c.post("/v1/chat/completions", json={"messages": msgs, "n": 2, "stream": True}).status_code == 400
+        assert c.post("/v1/chat/completions", json={"messages": msgs, "n": 0}).status_code == 400
+        r = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 2,
+                                                 "logit_bias": {"50": 5, "7": -300}})
+        assert r.status_code == 200 and seen[-1].logit_bias == {50: 5.0, 7: -100.0}
+        assert c.post("/v1/chat/completions", json={"messages": msgs,
+                                                    "logit_bias": {"a": 1}}).status_code == 400
+    ae.shutdown()

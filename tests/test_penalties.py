@@ -38,3 +38,18 @@ def test_presence_penalty_stops_repeats_greedy():
     assert len(set(pen)) == len(pen)                       # never the same token twice
     assert len(set(plain)) < len(plain)                    # the random model does repeat
     assert pen[0] == plain[0]                              # nothing generated yet: same first token
+
+
+def test_logit_bias_table_and_engine():
+    from swarmllm_b200.engine.sampling import SamplingParams, penalty_table
+    p = SamplingParams(logit_bias={5: 2.0, 9: -1.0})
+    assert p.penalized
+    off, tok, val = penalty_table([SamplingParams(), p], None)   # no history needed
+    assert off.tolist() == [0, 0, 2] and dict(zip(tok.tolist(), val.tolist())) == {5: -2.0, 9: 1.0}
+    q = SamplingParams(frequency_penalty=1.0, logit_bias={3: 0.5})
+    off, tok, val = penalty_table([q], [collections.Counter({3: 2, 4: 1})])
+    assert dict(zip(tok.tolist(), val.tolist())) == {3: 1.5, 4: 1.0}   # 2 * 1.0 - 0.5, 1 * 1.0
+    from swarmllm_b200.engine import SamplingParams as SP
+    eng = _engine()
+    out = eng.generate([list(range(3, 20))], SP(max_tokens=6, logit_bias={42: 100.0}))[0].token_ids
+    assert out == [42] * 6
