@@ -227,3 +227,21 @@ def test_json_constraint_gpu_graph_path():
         for o in outs:
             text = tok.decode([t for t in o.token_ids if t != tok.eos_id])
             assert text.lstrip().startswith("{") and JsonPrefix().feed(text), text
+
+
+def test_logit_bias_and_penalties_gpu_engine():
+    """Logit adjustments on the GPU engine (eager sampling path, the
+    apply_penalties kernel): a +100 bias pins greedy decoding to one token; a
+    huge presence penalty never repeats a token."""
+    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = _cfg()
+    eng = LLMEngine.from_config(cfg, DEV, EngineConfig(max_model_len=256, max_running=4,
+                                                       max_step_tokens=128, prefill_chunk=64,
+                                                       graph_sizes=(1, 2, 4)),
+                                source=RandomSource(cfg, seed=5))
+    prompt = np.random.default_rng(4).integers(0, cfg.vocab, 20).tolist()
+    out = eng.generate([prompt], SamplingParams(max_tokens=6, logit_bias={42: 100.0}))[0].token_ids
+    assert out == [42] * 6
+    out = eng.generate([prompt], SamplingParams(max_tokens=30, presence_penalty=1e4))[0].token_ids
+    assert len(set(out)) == len(out)
