@@ -740,6 +740,7 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
     async def metrics():
         e = aengine.engine
         aengine.metrics.set_kv(e.bm.num_free(), e.bm.num_pages)
+        aengine.metrics.set_engine(e, aengine.ready)
         return PlainTextResponse(aengine.metrics.render(), media_type="text/plain; version=0.0.4")
 
     # ------------------------------------------------------------------ prefix KV snapshots

@@ -27,11 +27,26 @@ class Metrics:
                                 buckets=(0.001, 0.0025, 0.005, 0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1))
         self.kv_free = Gauge("swarmllm_kv_pages_free", "Free KV pages", registry=r)
         self.kv_total = Gauge("swarmllm_kv_pages_total", "KV pages", registry=r)
+        self.running = Gauge("swarmllm_requests_running", "Requests in the running batch", registry=r)
+        self.waiting = Gauge("swarmllm_requests_waiting", "Requests waiting for admission",
+                             registry=r)
+        self.prefix_hits = Gauge("swarmllm_prefix_cache_hit_tokens",
+                                 "Prompt tokens served from the prefix cache since start", registry=r)
+        self.preemptions = Gauge("swarmllm_preemptions", "Requests preempted since start", registry=r)
+        self.ready = Gauge("swarmllm_ready", "1 when the node accepts inference", registry=r)
         # recent window for the admin views: (wall time, step seconds, tokens), TTFTs
         self.recent_steps: collections.deque = collections.deque(maxlen=4096)
         self.recent_ttft: collections.deque = collections.deque(maxlen=1024)
         self.n_started = self.n_done = self.n_tokens = 0
         self.t0 = time.time()
+
+    def set_engine(self, engine, ready: bool):
+        """Scheduler and cache state, read when /metrics is scraped."""
+        self.running.set(engine.sched.num_running)
+        self.waiting.set(engine.sched.num_waiting)
+        self.prefix_hits.set(engine.bm.prefix_hit_tokens)
+        self.preemptions.set(getattr(engine.sched, "num_preemptions", 0))
+        self.ready.set(1 if ready else 0)
 
     def requests_started(self):
         self.req_total.inc()

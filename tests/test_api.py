@@ -63,6 +63,10 @@ def test_health_metrics_status(client):
     assert client.get("/health/ready").status_code == 200
     m = client.get("/metrics").text
     assert "swarmllm_inference_requests_total" in m and "swarmllm_kv_pages_free" in m
+    for name in ("swarmllm_requests_running", "swarmllm_requests_waiting",
+                 "swarmllm_prefix_cache_hit_tokens", "swarmllm_preemptions"):
+        assert name in m, name
+    assert "swarmllm_ready 1.0" in m
     s = client.get("/api/status").json()
     assert s["kv_pages"] > 0
 
