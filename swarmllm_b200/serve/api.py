@@ -12,6 +12,7 @@ src/api/openai/streaming.rs:1431, src/api/anthropic/):
   POST/GET/DELETE /mcp         (Model Context Protocol server: serve/mcp.py)
   POST /v1/embeddings          (mean-pooled, L2-normalised input embeddings)
   GET  /v1/models              (the base model and every loaded LoRA adapter)
+  GET  /v1/models/{id}, POST /v1/messages/count_tokens
   GET  /health, /health/ready, /metrics (Prometheus), /api/status, /v1/status
   POST /api/prefix/export, /api/prefix/import   (prefix-KV snapshots, engine/prefix_share.py)
   /api/admin/*                 (stats, performance, config, models, lora,
@@ -708,6 +709,26 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
     async def models():
         return {"object": "list", "data": [{"id": m, "object": "model", "owned_by": "local",
                                             "max_model_len": max_model_len} for m in S.models()]}
+
+    @app.get("/v1/models/{mid:path}")
+    async def model_one(mid: str):
+        if mid not in S.models() and S.lora_of({"model": mid}) is None:
+            raise ApiError(404, f"The model '{mid}' does not exist")
+        return {"id": mid, "object": "model", "owned_by": "local", "max_model_len": max_model_len}
+
+    @app.post("/v1/messages/count_tokens")
+    async def count_tokens(request: Request):
+        """Anthropic token count of a messages request (system, tools and images included)."""
+        body = await body_of(request)
+        msgs = list(body.get("messages") or [])
+        if not msgs:
+            raise ApiError(400, "messages is required")
+        sysmsg = body.get("system")
+        if sysmsg:
+            msgs = [{"role": "system", "content": sysmsg if isinstance(sysmsg, str) else
+                     "".join(b.get("text", "") for b in sysmsg)}] + msgs
+        ids, _, images = S.prepare(msgs, tools_from_anthropic(body.get("tools")), body.get("tool_choice"))
+        return {"input_tokens": S.prompt_len(ids, images)}
 
     @app.get("/health")
     async def health():

@@ -517,3 +517,19 @@ def test_n_choices_and_logit_bias_parameters():
         assert c.post("/v1/chat/completions", json={"messages": msgs,
                                                     "logit_bias": {"a": 1}}).status_code == 400
     ae.shutdown()
+
+
+def test_model_retrieve_and_count_tokens():
+    c, ae, eng = _client("x")
+    with c:
+        assert c.get("/v1/models/m").json()["id"] == "m"
+        assert c.get("/v1/models/m:ad1").status_code == 200        # a LoRA adapter of the base
+        assert c.get("/v1/models/other").status_code == 404
+        r = c.post("/v1/messages/count_tokens", json={"model": "m", "system": "be brief",
+                                                      "messages": [{"role": "user", "content": "hello"}]})
+        n = r.json()["input_tokens"]
+        r2 = c.post("/v1/messages/count_tokens", json={"model": "m",
+                                                       "messages": [{"role": "user", "content": "hello"}]})
+        assert r.status_code == 200 and n > r2.json()["input_tokens"] > 5
+        assert c.post("/v1/messages/count_tokens", json={"messages": []}).status_code == 400
+    ae.shutdown()
