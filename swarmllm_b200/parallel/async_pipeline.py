@@ -48,6 +48,8 @@ _STEP, _STOP = 1, 2
 
 
 class AsyncPipelineEngine:
+    segments_served = 0    # layer-range forwards this rank ran (swarmllm_segments_served_total)
+    bytes_sent = 0         # bytes this rank sent to other ranks (swarmllm_network_bytes_total)
     def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, source_factory, device,
                  tp: int = 1, waves: int | None = None):
         self.cfg, self.ecfg = cfg, ecfg
@@ -133,6 +135,7 @@ class AsyncPipelineEngine:
 
     # ------------------------------------------------------------------ plumbing
     def _isend(self, t: torch.Tensor, dst: int):
+        self.bytes_sent += t.numel() * t.element_size()
         self._pending.append((dist.isend(t, dst), t))
         while len(self._pending) > 8:
             req, _ = self._pending.popleft()
@@ -183,6 +186,7 @@ class AsyncPipelineEngine:
             if grp is not None:
                 batch.groups = (t(grp[0]), t(grp[1]), grp[2])
         out = self.model.forward(batch, self.kv, self.ctx, h_in)
+        self.segments_served += 1
         return out, positions[samp_rows] if len(samp_rows) else positions[:0]
 
     def _recv_msg(self, src: int):

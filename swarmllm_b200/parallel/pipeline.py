@@ -62,6 +62,8 @@ class _MB:
 
 
 class PipelineEngine:
+    segments_served = 0    # layer-range forwards this rank ran (swarmllm_segments_served_total)
+    bytes_sent = 0         # bytes this rank sent to other ranks (swarmllm_network_bytes_total)
     """Same API as LLMEngine (add_request / step / generate), run by every rank
     in lockstep; only rank 0 accepts requests and returns results."""
 
@@ -215,9 +217,11 @@ class PipelineEngine:
                 h_in = torch.empty(rows, H, dtype=self.comm_dtype, device=dev)
                 dist.recv(h_in, self.rank - self.tp, group=self.group)
             out = self.model.forward(batch, self.kv, self.ctx, h_in)
+            self.segments_served += 1
             if not self.last:
                 # own buffer: the model's activation buffer is reused by the next micro-batch
                 h = out.to(self.comm_dtype).clone()
+                self.bytes_sent += h.numel() * h.element_size()
                 req = dist.isend(h, self.rank + self.tp, group=self.group)
                 pending.append((req, h))
             elif mb.n_sample and self.lane == 0:
@@ -235,7 +239,9 @@ class PipelineEngine:
         n_samp_total = sum(mb.n_sample for mb in mbs)
         last_lane0 = (self.n_stages - 1) * self.tp  # global rank that samples
         if self.last and self.lane == 0 and not self.root and n_samp_total:
-            dist.send(torch.cat(sampled_all).contiguous(), 0, group=self.group)
+            toks = torch.cat(sampled_all).contiguous()
+            self.bytes_sent += toks.numel() * toks.element_size()
+            dist.send(toks, 0, group=self.group)
         for req, _ in pending:
             req.wait()
         if self.root:

@@ -46,6 +46,7 @@ def _worker(rank, world, port, out_dir, micro, n_prompts, prompt_len, gen):
         torch.save(eng.record_logits, os.path.join(out_dir, f"logits_w{world}.pt"))
     if eng.first:
         torch.save(toks, os.path.join(out_dir, f"tokens_w{world}.pt"))
+        torch.save((eng.segments_served, eng.bytes_sent), os.path.join(out_dir, f"stats_w{world}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -60,7 +61,9 @@ def split_check(world: int = 2, micro: int = 2, n_prompts: int = 4, prompt_len: 
                                nprocs=w, join=True, start_method="spawn")
         t1, t2 = (torch.load(os.path.join(d, f"tokens_w{w}.pt")) for w in (1, world))
         l1, l2 = (torch.load(os.path.join(d, f"logits_w{w}.pt")) for w in (1, world))
+        segs, sent = torch.load(os.path.join(d, f"stats_w{world}.pt"))
     worst = max((float((a - b).abs().max()) for a, b in zip(l1, l2)), default=float("inf"))
     ok = t1 == t2 and len(l1) == len(l2) and worst <= 1e-5
     return {"world": world, "tokens_equal": t1 == t2, "steps": len(l1),
+            "first_stage_segments": segs, "first_stage_bytes_sent": sent,
             "max_logit_diff": worst, "tokens": t1, "ok": ok}

@@ -34,6 +34,10 @@ class Metrics:
                                  "Prompt tokens served from the prefix cache since start", registry=r)
         self.preemptions = Gauge("swarmllm_preemptions", "Requests preempted since start", registry=r)
         self.ready = Gauge("swarmllm_ready", "1 when the node accepts inference", registry=r)
+        self.segments = Gauge("swarmllm_segments_served_total",
+                              "Layer-range forwards run by this rank's pipeline stage", registry=r)
+        self.net_bytes = Gauge("swarmllm_network_bytes_total",
+                               "Bytes this rank sent to other ranks", registry=r)
         # recent window for the admin views: (wall time, step seconds, tokens), TTFTs
         self.recent_steps: collections.deque = collections.deque(maxlen=4096)
         self.recent_ttft: collections.deque = collections.deque(maxlen=1024)
@@ -47,6 +51,8 @@ class Metrics:
         self.prefix_hits.set(engine.bm.prefix_hit_tokens)
         self.preemptions.set(getattr(engine.sched, "num_preemptions", 0))
         self.ready.set(1 if ready else 0)
+        self.segments.set(getattr(engine, "segments_served", engine.steps))
+        self.net_bytes.set(getattr(engine, "bytes_sent", 0))
 
     def requests_started(self):
         self.req_total.inc()

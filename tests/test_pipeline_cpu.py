@@ -19,6 +19,8 @@ def test_two_peer_split_matches_single_peer():
     assert all(len(t) == 64 for t in r["tokens"])
     assert r["max_logit_diff"] <= 1e-5, r["max_logit_diff"]
     assert r["ok"]
+    # the first stage ran forwards and sent its activations on
+    assert r["first_stage_segments"] > 0 and r["first_stage_bytes_sent"] > 0
 
 
 def test_stage_bounds():
