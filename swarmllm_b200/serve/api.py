@@ -623,8 +623,10 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
         rs = await asyncio.gather(*[S.run(ids, v, S.stops(body), None, lora)
                                     for v in S.variants(sp, n)])
         n_out = sum(r.n_out for r in rs)
+        # echo: the prompt text ahead of each completion
+        head = tokenizer.decode([t for t in ids if t != S.eos]) if body.get("echo") else ""
         return {"id": cid, "object": "text_completion", "model": model_name,
-                "choices": [{"index": i, "text": r.text, "finish_reason": r.finish}
+                "choices": [{"index": i, "text": head + r.text, "finish_reason": r.finish}
                             for i, r in enumerate(rs)],
                 "usage": {"prompt_tokens": rs[0].n_prompt, "completion_tokens": n_out,
                           "total_tokens": rs[0].n_prompt + n_out}}

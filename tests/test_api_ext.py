@@ -533,3 +533,13 @@ def test_model_retrieve_and_count_tokens():
         assert r.status_code == 200 and n > r2.json()["input_tokens"] > 5
         assert c.post("/v1/messages/count_tokens", json={"messages": []}).status_code == 400
     ae.shutdown()
+
+
+def test_completions_echo():
+    c, ae, eng = _client("ok")
+    with c:
+        r = c.post("/v1/completions", json={"prompt": "say:", "max_tokens": 5, "echo": True})
+        assert r.json()["choices"][0]["text"] == "say:ok"
+        r = c.post("/v1/completions", json={"prompt": "say:", "max_tokens": 5})
+        assert r.json()["choices"][0]["text"] == "ok"
+    ae.shutdown()
