@@ -41,6 +41,9 @@ NVCC_FLAGS = [
 ]
 if os.environ.get("SWARMLLM_PTXAS_VERBOSE"):
     NVCC_FLAGS += ["-Xptxas", "-v"]
+if os.environ.get("SWARMLLM_KERNEL_TRACE"):
+    # Per-unit %globaltimer timelines of the GEMM / attention kernels (profiling only).
+    NVCC_FLAGS += ["-DSWARMLLM_KERNEL_TRACE=1"]
 if os.environ.get("SWARMLLM_DEVICE_CHECKS"):
     # Device-side bounds checks (record the bad index, skip the access).
     NVCC_FLAGS += ["-DSWARMLLM_DEVICE_CHECKS=1"]

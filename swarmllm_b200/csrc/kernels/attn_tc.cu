@@ -74,11 +74,19 @@ struct AttnTcArgs {
   unsigned long long* trace;   // debug: per-tile event timestamps of CTA (0,0,0)
 };
 
+// Debug timeline of CTA (0,0,0) (see attn_set_trace); compiled in only with
+// -DSWARMLLM_KERNEL_TRACE (setup.py: SWARMLLM_KERNEL_TRACE=1).
+#ifdef SWARMLLM_KERNEL_TRACE
 #define ATRACE(a, j, ev)                                                                      \
   do {                                                                                       \
     if ((a).trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && (j) < 64)      \
       (a).trace[(j) * 8 + (ev)] = globaltimer();                                             \
   } while (0)
+#else
+#define ATRACE(a, j, ev) \
+  do {                   \
+  } while (0)
+#endif
 
 SW_DEVICE float exp2_approx(float x) {
   float y;
@@ -567,17 +575,11 @@ template <int D>
 static int launch_d(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm,
                     const AttnTcArgs& a, int G, cudaStream_t s) {
   using C = AttnCfg<D>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_tc_kernel<D, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_tc_kernel<D, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_tc_kernel<D, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM) != cudaSuccess)
-      return -3;
-    attr = true;
-  }
+  static unsigned long long done1 = 0, done_tree = 0, done4 = 0;
+  if (!smem_attr_once(attn_tc_kernel<D, false, 1>, C::SMEM, &done1) ||
+      !smem_attr_once(attn_tc_kernel<D, true, 1>, C::SMEM, &done_tree) ||
+      !smem_attr_once(attn_tc_kernel<D, false, 4>, C::SMEM, &done4))
+    return -3;
   dim3 grid(G, a.n_kv, a.n_splits);
   if (a.tree_mask != nullptr)
     attn_tc_kernel<D, true, 1><<<grid, C::THREADS, C::SMEM, s>>>(qm, km, vm, a);

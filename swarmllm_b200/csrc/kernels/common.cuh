@@ -17,6 +17,22 @@ namespace swarm {
 
 constexpr int kWarp = 32;
 
+// cudaFuncSetAttribute applies to the device current at the call, so a launcher
+// that raises a kernel's dynamic shared-memory limit must do it once on every
+// device it launches on.  `done` is the launcher's bit mask of devices already
+// set (up to 64 devices); returns false if the attribute could not be set.
+template <typename Kernel>
+inline bool smem_attr_once(Kernel* fn, int bytes, unsigned long long* done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  const unsigned long long bit = 1ull << dev;
+  if (__atomic_load_n(done, __ATOMIC_ACQUIRE) & bit) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return false;
+  __atomic_fetch_or(done, bit, __ATOMIC_RELEASE);
+  return true;
+}
+
 SW_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

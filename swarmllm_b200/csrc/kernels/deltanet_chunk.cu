@@ -320,13 +320,8 @@ int launch_delta_chunk(const float* qkv, int C, int nk, int nv, int D, const Gem
   if (S <= 0 || T <= 0) return 0;
   if (D != kDk || nv % nk) return -1;
   const int smem = (int)sizeof(ChunkSmem);
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(delta_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem) != cudaSuccess)
-      return -3;
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  if (!smem_attr_once(delta_chunk_kernel, smem, &attr_done)) return -3;
   delta_chunk_kernel<<<dim3(S, nv, kDk / kDvg), kChunkThreads, smem, s>>>(
       qkv, C, nk, nv, gba, dt_bias, A, state, (const int4*)seqs, o_raw);
   const int warps = T * nv;

@@ -206,13 +206,8 @@ template <int N>
 static int dense_launch_n(const CUtensorMap& wm, const CUtensorMap& xm, const DGemmArgs& a,
                           int ctas, cudaStream_t s) {
   using C = DCfg<N>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(dense_gemm_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM) != cudaSuccess)
-      return -3;
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  if (!smem_attr_once(dense_gemm_tc_kernel<N>, C::SMEM, &attr_done)) return -3;
   dense_gemm_tc_kernel<N><<<ctas, C::THREADS, C::SMEM, s>>>(wm, xm, a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

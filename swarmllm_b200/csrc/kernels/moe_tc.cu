@@ -625,13 +625,8 @@ int launch_moe_scatter(const __half* x, int x_stride, int H, const int32_t* ids,
 template <int N, int FMT, int EPI>
 static int moe_launch_n(const CUtensorMap& map, const MoeGemmArgs& a, int ctas, cudaStream_t s) {
   using C = MCfg<N, FMT>;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(moe_gemm_tc_kernel<N, FMT, EPI>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
-      return -3;
-    attr = true;
-  }
+  static unsigned long long attr_done = 0;
+  if (!smem_attr_once(moe_gemm_tc_kernel<N, FMT, EPI>, C::SMEM, &attr_done)) return -3;
   moe_gemm_tc_kernel<N, FMT, EPI><<<ctas, C::THREADS, C::SMEM, s>>>(map, a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

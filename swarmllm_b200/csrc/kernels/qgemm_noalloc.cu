@@ -16,9 +16,16 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 // Device address of g_noalloc_scratch per device (the host-side symbol is only
-// a stand-in; it must never be passed to a kernel).
+// a stand-in; it must never be passed to a kernel).  These caches are written
+// without a lock: two threads setting up the same device at once both store
+// the same values, so the race is benign.
 void* g_scratch_dev[kMaxDevices] = {nullptr};
 int g_num_sms[kMaxDevices] = {0};
+
+int* status_of(int dev) {
+  return reinterpret_cast<int*>(static_cast<unsigned char*>(g_scratch_dev[dev]) +
+                                SWARM_NOALLOC_SCRATCH_FLOATS * 4u);
+}
 
 int setup_device(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return SWARM_NOALLOC_ERR_SETUP;
@@ -64,8 +71,7 @@ extern "C" int swarm_q4k_gemm_noalloc(const void* w_packed, int rows, int K, con
   if (need > SWARM_NOALLOC_SCRATCH_FLOATS) return SWARM_NOALLOC_ERR_TOO_LARGE;
 
   float* partials = static_cast<float*>(g_scratch_dev[dev]);
-  int* status = reinterpret_cast<int*>(static_cast<unsigned char*>(g_scratch_dev[dev]) +
-                                       SWARM_NOALLOC_SCRATCH_FLOATS * 4u);
+  int* status = status_of(dev);
   // The status word must start at zero for every call (timed-out waits set it).
   if (cudaMemsetAsync(status, 0, 32, stream) != cudaSuccess) return SWARM_NOALLOC_ERR_LAUNCH;
   swarm::GemmOut g{};
@@ -74,6 +80,21 @@ extern "C" int swarm_q4k_gemm_noalloc(const void* w_packed, int rows, int K, con
   if (rc != 0) return SWARM_NOALLOC_ERR_LAUNCH;
   launch_epi_copy(g, nullptr, out, out_stride, stream);
   return cudaPeekAtLastError() == cudaSuccess ? SWARM_NOALLOC_OK : SWARM_NOALLOC_ERR_LAUNCH;
+}
+
+extern "C" int swarm_q4k_gemm_noalloc_status(int* host_status8, cudaStream_t stream) {
+  if (host_status8 == nullptr) return SWARM_NOALLOC_ERR_SHAPE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SWARM_NOALLOC_ERR_SETUP;
+  const int rc_setup = setup_device(dev);
+  if (rc_setup != SWARM_NOALLOC_OK) return rc_setup;
+  // Ordered after the caller's GEMM on `stream`; the host buffer is pageable
+  // memory of the caller's, so the copy is synchronous with respect to it.
+  if (cudaMemcpyAsync(host_status8, status_of(dev), 32, cudaMemcpyDeviceToHost, stream) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return SWARM_NOALLOC_ERR_LAUNCH;
+  return host_status8[0] == 0 ? SWARM_NOALLOC_OK : SWARM_NOALLOC_ERR_KERNEL;
 }
 
 extern "C" const char* swarm_q4k_gemm_noalloc_error(int code) {
@@ -87,6 +108,9 @@ extern "C" const char* swarm_q4k_gemm_noalloc_error(int code) {
     case SWARM_NOALLOC_ERR_SETUP:
       return "setup failed: could not get the device address of the static scratch or the SM count";
     case SWARM_NOALLOC_ERR_LAUNCH: return "kernel launch failed";
+    case SWARM_NOALLOC_ERR_KERNEL:
+      return "the GEMM gave up on a bounded wait inside the kernel; the output of that call is "
+             "invalid (status word: [0] code, [1] block, [2..3] details)";
     default: return "unknown error code";
   }
 }

@@ -31,6 +31,14 @@
 //    are read, so nothing else needs clearing.
 //  * A problem whose partial sums need more than the scratch holds is
 //    rejected with SWARM_NOALLOC_ERR_TOO_LARGE before anything is launched.
+//  * swarm_q4k_gemm_noalloc returns once the work is queued; it cannot see
+//    what happens on the GPU.  Every wait inside the GEMM is bounded, and a
+//    wait that runs out records a code in the status word and ends the kernel
+//    early.  swarm_q4k_gemm_noalloc_status(host_status8, stream) waits for the
+//    stream, copies that status word (8 ints) to the caller's host buffer and
+//    returns SWARM_NOALLOC_ERR_KERNEL when it is set: the output of that call
+//    is then invalid.  Read it before the next call on the device, which
+//    clears the word again.
 #pragma once
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -43,6 +51,7 @@
 #define SWARM_NOALLOC_ERR_SHAPE -11       // rows % 128 or K % 256 not zero, or T <= 0
 #define SWARM_NOALLOC_ERR_SETUP -12       // cudaGetSymbolAddress / device query failed
 #define SWARM_NOALLOC_ERR_LAUNCH -13      // the GEMM or epilogue launch failed
+#define SWARM_NOALLOC_ERR_KERNEL -14      // the last call's kernel recorded an error (status)
 
 #ifdef __cplusplus
 extern "C" {
@@ -51,6 +60,12 @@ extern "C" {
 __attribute__((visibility("default"))) int swarm_q4k_gemm_noalloc(
     const void* w_packed, int rows, int K, const __half* x, int x_stride, int T, float* out,
     int out_stride, cudaStream_t stream);
+
+// Status of the most recent call on the current device: waits for `stream`,
+// copies the 8-int status word into host_status8 and returns SWARM_NOALLOC_OK
+// (status clear: the output is valid) or SWARM_NOALLOC_ERR_KERNEL (invalid).
+__attribute__((visibility("default"))) int swarm_q4k_gemm_noalloc_status(int* host_status8,
+                                                                         cudaStream_t stream);
 
 // Human-readable text for a return code of swarm_q4k_gemm_noalloc.
 __attribute__((visibility("default"))) const char* swarm_q4k_gemm_noalloc_error(int code);

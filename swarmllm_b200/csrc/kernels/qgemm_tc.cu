@@ -92,11 +92,18 @@ struct QGemmArgs {
 };
 
 // Debug timeline of CTA 0 (see qgemm_set_trace): trace[unit*8 + event] = %globaltimer.
+// Compiled in only with -DSWARMLLM_KERNEL_TRACE (setup.py: SWARMLLM_KERNEL_TRACE=1).
+#ifdef SWARMLLM_KERNEL_TRACE
 #define QTRACE(tr, unit, ev)                                                           \
   do {                                                                                 \
     if ((tr) != nullptr && blockIdx.x == 0 && (unit) < 512) (tr)[(unit) * 8 + (ev)] = \
         globaltimer();                                                                 \
   } while (0)
+#else
+#define QTRACE(tr, unit, ev) \
+  do {                       \
+  } while (0)
+#endif
 
 template <int N>
 __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
@@ -432,13 +439,8 @@ void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_
 template <int N>
 static int launch_n(const CUtensorMap& map, const QGemmArgs& a, int n_ctas, cudaStream_t s) {
   using C = QCfg<N>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(qgemm_q4k_tc_kernel<N>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
-      return -3;
-    attr_set = true;
-  }
+  static unsigned long long attr_done = 0;
+  if (!smem_attr_once(qgemm_q4k_tc_kernel<N>, C::SMEM, &attr_done)) return -3;
   qgemm_q4k_tc_kernel<N><<<n_ctas, C::THREADS, C::SMEM, s>>>(map, a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

@@ -35,6 +35,7 @@ import dataclasses
 import itertools
 import os
 import json
+import secrets
 import queue
 import threading
 import time
@@ -300,10 +301,22 @@ class Serving:
                               constraint=constraint, logit_bias=bias,
                               top_p=float(body.get("top_p", 1.0) or 1.0),
                               top_k=int(body.get("top_k", 0) or 0),
-                              seed=int(body.get("seed", 0) or 0), eos_token_id=int(self.eos),
+                              seed=self.seed_of(body), eos_token_id=int(self.eos),
                               ignore_eos=bool(body.get("ignore_eos", False)),
                               frequency_penalty=float(body.get("frequency_penalty", 0.0) or 0.0),
                               presence_penalty=float(body.get("presence_penalty", 0.0) or 0.0))
+
+    @staticmethod
+    def seed_of(body: dict) -> int:
+        """The client's seed, or a fresh random one: unseeded sampled requests
+        must not all draw the same tokens for the same prompt."""
+        seed = body.get("seed")
+        if seed is None:
+            return secrets.randbits(62)
+        try:
+            return int(seed)
+        except (TypeError, ValueError):
+            raise ApiError(400, "seed must be an integer")
 
     def piece(self, tok: int) -> str:
         """Text of one token (cached: the JSON constraint asks for many)."""
@@ -602,14 +615,35 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
     async def completions(request: Request):
         body = await body_of(request)
         p = body.get("prompt", "")
-        ids = list(p) if isinstance(p, list) and p and isinstance(p[0], int) else tokenizer.encode(
-            p if isinstance(p, str) else "".join(p))
-        sp = S.params(body, len(ids))
+        # OpenAI prompt forms: a string, a token-id list, or a batch of either
+        # (each batch entry gets its own n choices, indexed prompt-major).
+        if isinstance(p, list) and p and all(isinstance(x, int) for x in p):
+            batch = [list(p)]
+        elif isinstance(p, list) and p and all(isinstance(x, (str, list)) for x in p):
+            batch = [list(x) if isinstance(x, list) else tokenizer.encode(x) for x in p]
+            if not all(all(isinstance(t, int) for t in b) for b in batch):
+                raise ApiError(400, "prompt lists must hold strings or token-id lists")
+        elif isinstance(p, str):
+            batch = [tokenizer.encode(p)]
+        else:
+            raise ApiError(400, "prompt must be a string, a token-id list, or a list of those")
         n = S.n_of(body)
         lora = S.lora_of(body)
         cid = "cmpl-" + uuid.uuid4().hex[:24]
+        echo = bool(body.get("echo"))
+
+        def head_of(ids):  # echo: the prompt text ahead of each completion
+            return tokenizer.decode([t for t in ids if t != S.eos]) if echo else ""
         if body.get("stream"):
+            if len(batch) != 1:
+                raise ApiError(400, "streaming serves one prompt per request")
+            ids = batch[0]
+            sp = S.params(body, len(ids))
+
             async def gen():
+                if echo:
+                    yield sse({"id": cid, "object": "text_completion", "model": model_name,
+                               "choices": [{"index": 0, "text": head_of(ids), "finish_reason": None}]})
                 async for ev in S.stream(ids, sp, S.stops(body), None, lora):
                     if ev[0] == "text":
                         ch = {"id": cid, "object": "text_completion", "model": model_name,
@@ -620,16 +654,20 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
                     yield sse(ch)
                 yield "data: [DONE]\n\n"
             return StreamingResponse(gen(), media_type="text/event-stream")
-        rs = await asyncio.gather(*[S.run(ids, v, S.stops(body), None, lora)
-                                    for v in S.variants(sp, n)])
+        if len(batch) * n > S.MAX_N:
+            raise ApiError(400, f"at most {S.MAX_N} completions (prompts x n) per request")
+        jobs = []
+        for ids in batch:
+            sp = S.params(body, len(ids))
+            jobs += [(ids, v) for v in S.variants(sp, n)]
+        rs = await asyncio.gather(*[S.run(ids, v, S.stops(body), None, lora) for ids, v in jobs])
         n_out = sum(r.n_out for r in rs)
-        # echo: the prompt text ahead of each completion
-        head = tokenizer.decode([t for t in ids if t != S.eos]) if body.get("echo") else ""
+        n_prompt = sum(rs[i * n].n_prompt for i in range(len(batch)))
         return {"id": cid, "object": "text_completion", "model": model_name,
-                "choices": [{"index": i, "text": head + r.text, "finish_reason": r.finish}
-                            for i, r in enumerate(rs)],
-                "usage": {"prompt_tokens": rs[0].n_prompt, "completion_tokens": n_out,
-                          "total_tokens": rs[0].n_prompt + n_out}}
+                "choices": [{"index": i, "text": head_of(ids) + r.text, "finish_reason": r.finish}
+                            for i, ((ids, _), r) in enumerate(zip(jobs, rs))],
+                "usage": {"prompt_tokens": n_prompt, "completion_tokens": n_out,
+                          "total_tokens": n_prompt + n_out}}
 
     # ------------------------------------------------------------------ Anthropic messages
     @app.post("/v1/messages")

@@ -543,3 +543,47 @@ def test_completions_echo():
         r = c.post("/v1/completions", json={"prompt": "say:", "max_tokens": 5})
         assert r.json()["choices"][0]["text"] == "ok"
     ae.shutdown()
+
+
+def test_completions_stream_echo_and_prompt_batch():
+    c, ae, eng = _client("ok")
+    with c:
+        r = c.post("/v1/completions", json={"prompt": "say:", "max_tokens": 5, "echo": True,
+                                            "stream": True})
+        chunks = [json.loads(l[6:]) for l in r.text.splitlines()
+                  if l.startswith("data: ") and l != "data: [DONE]"]
+        text = "".join(ch["choices"][0]["text"] for ch in chunks)
+        assert chunks[0]["choices"][0]["text"] == "say:" and text == "say:ok"
+        # a batch of prompts: one choice per prompt (x n), indexed prompt-major
+        r = c.post("/v1/completions", json={"prompt": ["a:", "b:"], "max_tokens": 5,
+                                            "echo": True, "n": 2})
+        j = r.json()
+        assert r.status_code == 200
+        assert [ch["index"] for ch in j["choices"]] == [0, 1, 2, 3]
+        assert [ch["text"] for ch in j["choices"]] == ["a:ok", "a:ok", "b:ok", "b:ok"]
+        assert c.post("/v1/completions", json={"prompt": ["a", "b"], "stream": True}).status_code == 400
+        assert c.post("/v1/completions", json={"prompt": 5}).status_code == 400
+    ae.shutdown()
+
+
+def test_unseeded_requests_draw_fresh_seeds():
+    """Without a client seed every sampled request gets its own random seed,
+    so two unseeded requests are not forced to sample identical tokens."""
+    c, ae, eng = _client("hey")
+    seen = []
+    orig = eng.add_request
+
+    def spy(ids, sp, *a, **kw):
+        seen.append(sp)
+        return orig(ids, sp, *a, **kw)
+    eng.add_request = spy
+    msgs = [{"role": "user", "content": "x"}]
+    with c:
+        for _ in range(2):
+            assert c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 2,
+                                                        "temperature": 0.9}).status_code == 200
+        assert seen[-1].seed != seen[-2].seed
+        c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 2, "seed": 7})
+        assert seen[-1].seed == 7
+        assert c.post("/v1/chat/completions", json={"messages": msgs, "seed": "x"}).status_code == 400
+    ae.shutdown()

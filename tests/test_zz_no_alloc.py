@@ -36,7 +36,16 @@ def _lib():
     lib.swarm_q4k_gemm_noalloc_error.argtypes = [ctypes.c_int]
     lib.swarm_q4k_gemm_noalloc_scratch_need.restype = ctypes.c_longlong
     lib.swarm_q4k_gemm_noalloc_scratch_need.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    lib.swarm_q4k_gemm_noalloc_status.restype = ctypes.c_int
+    lib.swarm_q4k_gemm_noalloc_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
     return lib
+
+
+def _status(lib, stream):
+    """The status word of the last call (waits for the stream); 0 = output valid."""
+    st = (ctypes.c_int * 8)()
+    rc = lib.swarm_q4k_gemm_noalloc_status(ctypes.addressof(st), stream)
+    return rc, list(st)
 
 
 def _rel_err(a, b):
@@ -53,31 +62,41 @@ def _regular(lin, ws, x):
     return out
 
 
-@pytest.mark.parametrize("rows,K", [(1024, 4096), (512, 28672)])
-def test_noalloc_matches_regular_entry_point_twice(rows, K):
+# T = 1 and 2 take the CUDA-core GEMV branch of the entry point, 7 and 32 the
+# tensor-core GEMM; both share the static partial sums and status word.
+@pytest.mark.parametrize("rows,K,Ts", [(1024, 4096, (7, 32)), (512, 28672, (7, 32)),
+                                       (1024, 4096, (1, 2)), (640, 8192, (2, 1))])
+def test_noalloc_matches_regular_entry_point_twice(rows, K, Ts):
     from swarmllm_b200.gguf import quants as Q
     from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
     torch.cuda.set_device(0)
     lib = _lib()
-    rng = np.random.default_rng(rows + K)
+    rng = np.random.default_rng(rows + K + Ts[0])
     b = Q.quantize(rng.standard_normal((rows, K), dtype=np.float32) * 0.02, Q.Q4_K)
     lin = QLinear(b, Q.Q4_K, rows, K, DEV)
     ws = GemmWorkspace(DEV, 32, rows)
     stream = torch.cuda.current_stream().cuda_stream
-    for call, T in enumerate((7, 32)):  # two calls in a row with different inputs
+    wd = torch.from_numpy(Q.dequantize(b, Q.Q4_K))
+    for call, T in enumerate(Ts):  # two calls in a row with different inputs
         g = torch.Generator().manual_seed(100 + call)
-        x = (torch.randn(T, K, generator=g)).half().to(DEV)
-        out = torch.full((T, rows), float("nan"), dtype=torch.float32, device=DEV)
-        rc = lib.swarm_q4k_gemm_noalloc(lin.packed.data_ptr(), rows, K, x.data_ptr(), K, T,
-                                        out.data_ptr(), rows, stream)
+        # the second call reads a row-strided input and writes a row-strided output
+        xs, os_ = (K, rows) if call == 0 else (K + 64, rows + 32)
+        xbuf = torch.randn(T, xs, generator=g).half().to(DEV)
+        x = xbuf[:, :K]
+        obuf = torch.full((T, os_), float("nan"), dtype=torch.float32, device=DEV)
+        rc = lib.swarm_q4k_gemm_noalloc(lin.packed.data_ptr(), rows, K, xbuf.data_ptr(), xs, T,
+                                        obuf.data_ptr(), os_, stream)
         assert rc == 0, lib.swarm_q4k_gemm_noalloc_error(rc).decode()
-        ref = _regular(lin, ws, x)
+        rc, st = _status(lib, stream)
+        assert rc == 0 and st[0] == 0, (rc, st)
+        out = obuf[:, :rows]
+        assert torch.isnan(obuf[:, rows:]).all()  # nothing written past each output row
+        ref = _regular(lin, ws, x.contiguous())
         torch.cuda.synchronize()
         assert torch.isfinite(out).all()
-        assert _rel_err(out.cpu(), ref.cpu()) < 3e-3, call
+        assert _rel_err(out.cpu(), ref.cpu()) < 3e-3, (call, T)
         # and against the dequantized fp32 product
-        wd = torch.from_numpy(Q.dequantize(b, Q.Q4_K))
-        assert _rel_err(out.cpu(), x.cpu().float() @ wd.T) < 3e-3
+        assert _rel_err(out.cpu(), x.cpu().float() @ wd.T) < 3e-3, (call, T)
 
 
 def test_noalloc_rejects_oversized_problem():
