@@ -4,9 +4,16 @@ and batch 1, plus p50 TTFT of a 2048-token prompt, on N B200s of one node.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...       (N > 1)
 
-N = 1: the whole model on one GPU.  N > 1: pipeline stages over NCCL p2p
-(``swarmllm_b200.parallel.pipeline``), weak scaling: 32 sequences per stage
-in flight (global batch 32*N), micro-batched so every stage is busy.
+N = 1: the whole model on one GPU.  N > 1 (torchrun): the same global batch
+of 32 sequences (strong scaling) on a tensor-parallel and/or pipeline layout
+(``--tp`` ranks per stage, the rest pipeline stages over NCCL p2p; see
+``swarmllm_b200.parallel.bench_pp``).  The batch-1 figure is one sequence
+alone and the TTFT one 2048-token prompt alone, at every N.
+
+`vs_baseline` is null: the reference publishes no batch-32 figure for this
+model.  `vs_baseline_batch1` divides the batch-1 rate by the reference's
+published 70B figure (4.1 tok/s, batch 1, three computers over a WAN), which
+is on other hardware and only context.
 
 `value` is device time: CUDA events around exactly K decode steps on the
 launching stream, bracketed by barrier + synchronize, max over ranks.
@@ -197,8 +204,9 @@ def single_gpu(args):
                    f"decode tok/s at batch {B} (aggregate), {cfg.name}"),
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms32 / args.steps, 4),
-        "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": round(value / BASELINE_70B_TOKS, 2) if headline else None,
+        "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None,
+        "vs_baseline_batch1": round(args.steps / (ms1 / 1e3) / BASELINE_70B_TOKS, 2) if headline else None,
         "dtype": f"fp16/bf16 activations, fp32 accumulate, {wq} weights",
         "data": f"synthetic uniform-random token ids; random-init {wq} weights ({cfg.name} architecture)",
         "config": {"model": cfg.name, "layers": cfg.n_layers, "global_batch": B, "seq_len": P,

@@ -3,12 +3,13 @@ over N / tp stages (torchrun, one process per GPU, NCCL p2p between stages),
 tensor-parallel inside each stage when tp > 1, run by the wave-pipelined
 engine (parallel/async_pipeline.py).
 
-Weak scaling: `batch` sequences per stage -- one wave of `batch` sequences per
-stage, global batch batch * stages.  Device time: CUDA events on every rank
-around exactly K rounds (K wave steps per wave) with barrier + synchronize on
-both sides, reduced with MAX; the same rounds run through the public API
-(requests in, sampled tokens out), so the host wall time (MAX over ranks) is
-the end-to-end figure.
+Strong scaling: the global batch is `batch` sequences (32) at every N, split
+into min(stages, batch) waves; the batch-1 figure is one sequence alone, and
+the TTFT one prompt alone.  Device time: CUDA events on every rank around
+exactly K decode steps of every running sequence (K wave steps per non-empty
+wave) with barrier + synchronize on both sides, reduced with MAX; the same
+steps run through the public API (requests in, sampled tokens out), so the
+host wall time (MAX over ranks) is the end-to-end figure.
 """
 from __future__ import annotations
 
@@ -50,13 +51,13 @@ def pipeline_bench(args):
         cfg = cfg.scaled(n_layers=args.layers)
     tp = getattr(args, "tp", 1) or 1
     S = world // tp
-    Bw = args.batch                     # sequences per wave (= per stage)
+    B = args.batch                      # global batch (all waves together)
     P, G = args.prompt, args.gen
-    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=Bw * S, max_step_tokens=P,
-                        prefill_chunk=P, kv_pages=S * Bw * ((P + G + 64 + 15) // 16) + 64)
+    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=B, max_step_tokens=P,
+                        prefill_chunk=P, kv_pages=B * ((P + G + 64 + 15) // 16) + 64 * S)
     t0 = time.time()
     eng = AsyncPipelineEngine(cfg, ecfg, lambda: RandomSource(cfg, seed=1234, on_device=True),
-                              dev, tp=tp)
+                              dev, tp=tp, waves=min(S, B))
     torch.cuda.synchronize()
     dist.barrier()
     _log(rank, f"stages {eng.bounds} x tp{tp}, waves {eng.V}, init {time.time() - t0:.1f}s")
@@ -84,12 +85,13 @@ def pipeline_bench(args):
         rids = []
         if rank == 0:
             rids = [eng.add_request(rng.integers(0, cfg.vocab, P).tolist(), sp)
-                    for _ in range(batch * S)]
+                    for _ in range(batch)]
+        live = min(batch, eng.V)            # waves holding sequences
         t_pf = time.time()
         eng.run(stop_when=(lambda: all(len(eng.output(x)) > 0 for x in rids)) if rank == 0 else None)
-        _log(rank, f"batch {batch}/wave: prefill {time.time() - t_pf:.1f}s")
+        _log(rank, f"batch {batch}: prefill {time.time() - t_pf:.1f}s")
         if rank == 0:
-            target = eng.retired + args.warmup * S
+            target = eng.retired + args.warmup * live
             eng.run(stop_when=lambda: eng.retired >= target)
         else:
             eng.run()
@@ -100,7 +102,7 @@ def pipeline_bench(args):
             t = time.perf_counter()
             a.record()
             if rank == 0:
-                target = eng.retired + args.steps * S
+                target = eng.retired + args.steps * live
                 eng.run(stop_when=lambda: eng.retired >= target)
             else:
                 eng.run()
@@ -118,34 +120,36 @@ def pipeline_bench(args):
             eng.run()
         return ms, wall, cs.summary()
 
-    ms_b, wall_b, clocks = decode(Bw)
+    ms_b, wall_b, clocks = decode(B)
     ms_1, wall_1, _ = decode(1)
-    tokens = args.steps * S * Bw
+    tokens = args.steps * B
     value = tokens / (ms_b / 1e3)
-    launches = torch.tensor([eng.model.decode_launches() * args.steps * S], device=dev)
+    launches = torch.tensor([eng.model.decode_launches() * args.steps * min(B, eng.V)], device=dev)
     dist.all_reduce(launches)
     if rank == 0:
         line = {
-            "metric": f"decode tok/s at batch {Bw} per stage (aggregate), Llama-3.3-70B Q4_K",
+            "metric": f"decode tok/s at batch {B} (aggregate), Llama-3.3-70B Q4_K",
             "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_b / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": round(value / BASELINE_70B_TOKS, 2),
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None,
+            "vs_baseline_batch1": round(args.steps / (ms_1 / 1e3) / BASELINE_70B_TOKS, 2),
             "dtype": "fp16 activations, fp32 accumulate, Q4_K weights",
             "data": "synthetic uniform-random token ids; random-init Q4_K weights (llama-3.3-70b architecture)",
-            "config": {"model": cfg.name, "layers": cfg.n_layers, "global_batch": Bw * S,
+            "config": {"model": cfg.name, "layers": cfg.n_layers, "global_batch": B,
                        "seq_len": P, "gen_len": G,
                        "parallelism": f"pp{S}" + (f"xtp{tp}" if tp > 1 else ""),
                        "stages": eng.bounds, "waves": eng.V,
-                       "step": "one round = every wave advances one token",
+                       "step": "every running sequence advances one token",
                        "tp": "fused: GEMM epilogue pushes partials over NVLink" if tp > 1 else None,
                        "kv": "paged fp16, 16-token pages",
                        "l2": "no flush: weights streamed per step >> 126 MB L2"},
-            "decode_tok_s_batch1": round(args.steps * S / (ms_1 / 1e3), 2),
+            "decode_tok_s_batch1": round(args.steps / (ms_1 / 1e3), 2),
+            "ms_per_step_batch1": round(ms_1 / args.steps, 4),
             "ttft_p50_ms": round(statistics.median(ttfts[1:]), 2), "ttft_prompt_tokens": P,
             "e2e": {"value": round(tokens / wall_b, 2), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(S * 4 * (4 + eng.max_pages + 3) * Bw + 32 * S),
-                    "d2h_bytes_per_step": 4 * Bw * S},
+                    "h2d_bytes_per_step": int(4 * (4 + eng.max_pages + 3) * B + 32 * min(B, eng.V)),
+                    "d2h_bytes_per_step": 4 * B, "batch1_value": round(args.steps / wall_1, 2)},
             "gpu_launches": int(launches.item()),
             "clocks": clocks,
         }
