@@ -54,7 +54,11 @@ def parse():
     p.add_argument("--ttft-reps", type=int, default=3)
     p.add_argument("--chunk", type=int, default=0, help="prefill chunk (0: whole prompt)")
     p.add_argument("--tp", type=int, default=0,
-                   help="tensor-parallel ranks per pipeline stage (0: 2 on 8 GPUs, else 1)")
+                   help="tensor-parallel ranks per pipeline stage (0: all GPUs in one TP group)")
+    p.add_argument("--pp-layout", action="store_true",
+                   help="run tp == N through the wave-pipelined engine (one stage) instead")
+    p.add_argument("--advance", type=int, default=256,
+                   help="untimed decode steps before timing (mid-generation context; >= warmup)")
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the headline)")
     return p.parse_args()
 
@@ -66,8 +70,9 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
+    def __init__(self, gpu_index):
+        ids = gpu_index if isinstance(gpu_index, (list, tuple)) else [gpu_index]
+        self.idx = ",".join(str(i) for i in ids)
         self.samples = []
         self._stop = threading.Event()
         self._t = None
@@ -120,27 +125,16 @@ def log(msg):
     print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
 
 
-def single_gpu(args):
+def measure(eng, cfg, args, replay, gpu_ids, h2d_of, d2h_of):
+    """TTFT, then batch-B and batch-1 decode, on an engine driven from this
+    process (LLMEngine, or the root of a TpEngine).  `replay(batch, steps)`
+    runs `steps` captured decode graphs of `batch` rows and returns this rank's
+    device ms (CUDA events on the launching stream)."""
     import numpy as np
     import torch
 
-    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
-    from swarmllm_b200.models.config import preset
-
-    cfg = preset(args.model)
-    if args.layers:
-        cfg = cfg.scaled(n_layers=args.layers)
-    dev = torch.device("cuda:0")
-    torch.cuda.set_device(dev)
+    from swarmllm_b200.engine import SamplingParams
     B, P, G = args.batch, args.prompt, args.gen
-    chunk = args.chunk or P
-    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=B, max_step_tokens=chunk,
-                        prefill_chunk=chunk, graph_sizes=(1, B))
-    t0 = time.time()
-    eng = LLMEngine.from_config(cfg, dev, ecfg, seed=1234)
-    t_init = time.time() - t0
-    log(f"engine ready in {t_init:.1f}s; weights {eng.model.weight_bytes() / 1e9:.1f} GB, "
-        f"kv pages {eng.bm.num_pages}")
     rng = np.random.default_rng(0)
     sp = SamplingParams(max_tokens=G, ignore_eos=True)
 
@@ -157,31 +151,23 @@ def single_gpu(args):
                 break
         ttfts.append((time.perf_counter() - t) * 1e3)
         eng.release(rid)
-    ttft_p50 = statistics.median(ttfts[1:])  # first run includes one-time setup
     log(f"ttft runs (ms): {[round(t, 1) for t in ttfts]}")
 
     def decode_rate(batch: int, steps: int, warmup: int):
         rids = [eng.add_request(rng.integers(0, cfg.vocab, P).tolist(), sp) for _ in range(batch)]
-        # run until every sequence is decoding
-        t_pf = time.time()
-        while eng.sched.num_waiting or any(len(eng.output(r)) == 0 for r in rids):
-            eng.step()
-        log(f"batch {batch}: prefill of {batch}x{P} tokens took {time.time() - t_pf:.1f}s")
-        for _ in range(warmup):
-            eng.step()
-        runner = eng.runner
-        g, _, _ = runner.graphs[batch]
-        # device-timed: K graph replays of the decode step (inputs already resident)
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])
-                          if os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0].isdigit() else 0) as cs:
-            a.record()
-            for _ in range(steps):
-                g.replay()
-            b.record()
+        with ClockSampler(gpu_ids) as cs:
+            # run until every sequence is decoding
+            t_pf = time.time()
+            while eng.sched.num_waiting or any(len(eng.output(r)) == 0 for r in rids):
+                eng.step()
+            log(f"batch {batch}: prefill of {batch}x{P} tokens took {time.time() - t_pf:.1f}s")
+            # untimed steps: the W warm-up steps, then on to mid-generation context
+            for _ in range(max(warmup, args.advance)):
+                eng.step()
+            ctx = P + len(eng.output(rids[0]))
+            # device-timed: K graph replays of the decode step (inputs already resident)
             torch.cuda.synchronize()
-            dev_ms = a.elapsed_time(b)
+            dev_ms = replay(batch, steps)
             # end to end through the public API (H2D inputs + D2H tokens every step)
             torch.cuda.synchronize()
             t = time.perf_counter()
@@ -191,41 +177,157 @@ def single_gpu(args):
         for r in rids:
             eng.abort(r)
             eng.release(r)
-        return dev_ms, e2e_s, cs.summary(), runner.h2d_bytes, runner.d2h_bytes
+        return dev_ms, e2e_s, cs.summary(), h2d_of(), d2h_of(), ctx
 
-    ms32, e2e32, clocks, h2d, d2h = decode_rate(B, args.steps, args.warmup)
-    ms1, e2e1, _, _, _ = decode_rate(1, args.steps, args.warmup)
-    value = B * args.steps / (ms32 / 1e3)
-    launches = eng.model.decode_launches() * args.steps
+    ms_b, e2e_b, clocks, h2d, d2h, ctx = decode_rate(B, args.steps, args.warmup)
+    ms1, e2e1, _, _, _, _ = decode_rate(1, args.steps, args.warmup)
+    return dict(ttfts=ttfts, ms_b=ms_b, e2e_b=e2e_b, clocks=clocks, h2d=h2d, d2h=d2h, ms1=ms1,
+                e2e1=e2e1, ctx=ctx)
+
+
+def result_line(cfg, args, m, n_gpus, parallelism, weight_gb, launches_per_step, extra=None):
+    B, P, G = args.batch, args.prompt, args.gen
+    value = B * args.steps / (m["ms_b"] / 1e3)
     headline = cfg.name == "llama-3.3-70b"
     wq = cfg.expert_qtype if cfg.n_experts else cfg.weight_qtype
+    b1 = args.steps / (m["ms1"] / 1e3)
     line = {
         "metric": (f"decode tok/s at batch {B} (aggregate), Llama-3.3-70B Q4_K" if headline else
                    f"decode tok/s at batch {B} (aggregate), {cfg.name}"),
-        "value": round(value, 2), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms32 / args.steps, 4),
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": n_gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(m["ms_b"] / args.steps, 4),
         "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None,
-        "vs_baseline_batch1": round(args.steps / (ms1 / 1e3) / BASELINE_70B_TOKS, 2) if headline else None,
+        "vs_baseline_batch1": round(b1 / BASELINE_70B_TOKS, 2) if headline else None,
         "dtype": f"fp16/bf16 activations, fp32 accumulate, {wq} weights",
         "data": f"synthetic uniform-random token ids; random-init {wq} weights ({cfg.name} architecture)",
         "config": {"model": cfg.name, "layers": cfg.n_layers, "global_batch": B, "seq_len": P,
-                   "gen_len": G, "parallelism": "single GPU", "kv": "paged fp16, 16-token pages",
-                   "l2": f"no flush: {eng.model.weight_bytes() / 1e9:.0f} GB of weights per model, "
-                         "streamed per step, >> 126 MB L2"},
-        "decode_tok_s_batch1": round(args.steps / (ms1 / 1e3), 2),
-        "ms_per_step_batch1": round(ms1 / args.steps, 4),
-        "ttft_p50_ms": round(ttft_p50, 2), "ttft_prompt_tokens": P,
-        "e2e": {"value": round(B * args.steps / e2e32, 2), "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "batch1_value": round(args.steps / e2e1, 2)},
-        "gpu_launches": launches,
-        "clocks": clocks,
-        "init_s": round(t_init, 1),
+                   "gen_len": G, "parallelism": parallelism, "kv": "paged fp16, 16-token pages",
+                   "context_at_timing": m["ctx"],
+                   "timing": "K replays of the captured decode step, CUDA events, max over ranks",
+                   "l2": f"no flush: {weight_gb:.0f} GB of weights per step, streamed, >> 126 MB L2"},
+        "decode_tok_s_batch1": round(b1, 2),
+        "ms_per_step_batch1": round(m["ms1"] / args.steps, 4),
+        "ttft_p50_ms": round(statistics.median(m["ttfts"][1:]), 2), "ttft_prompt_tokens": P,
+        "e2e": {"value": round(B * args.steps / m["e2e_b"], 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": m["h2d"], "d2h_bytes_per_step": m["d2h"],
+                "batch1_value": round(args.steps / m["e2e1"], 2)},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": m["clocks"],
     }
+    if extra:
+        line.update(extra)
     if args.layers:
         line["invalid"] = "layer count overridden (debug)"
+    return line
+
+
+def _visible_gpu(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    ids = [x for x in vis.split(",") if x.strip()]
+    return int(ids[local]) if local < len(ids) and ids[local].strip().isdigit() else local
+
+
+def _graph_replay(runner):
+    import torch
+
+    def replay(batch, steps):
+        g = runner.graphs[batch][0]
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b)
+    return replay
+
+
+def single_gpu(args):
+    import torch
+
+    from swarmllm_b200.engine import EngineConfig, LLMEngine
+    from swarmllm_b200.models.config import preset
+
+    cfg = preset(args.model)
+    if args.layers:
+        cfg = cfg.scaled(n_layers=args.layers)
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    B, P, G = args.batch, args.prompt, args.gen
+    chunk = args.chunk or P
+    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=B, max_step_tokens=chunk,
+                        prefill_chunk=chunk, graph_sizes=(1, B))
+    t0 = time.time()
+    eng = LLMEngine.from_config(cfg, dev, ecfg, seed=1234)
+    t_init = time.time() - t0
+    log(f"engine ready in {t_init:.1f}s; weights {eng.model.weight_bytes() / 1e9:.1f} GB, "
+        f"kv pages {eng.bm.num_pages}")
+    runner = eng.runner
+    m = measure(eng, cfg, args, _graph_replay(runner), [_visible_gpu(0)],
+                lambda: runner.h2d_bytes, lambda: runner.d2h_bytes)
+    line = result_line(cfg, args, m, 1, "single GPU", eng.model.weight_bytes() / 1e9,
+                       eng.model.decode_launches(), {"init_s": round(t_init, 1)})
     print(json.dumps(line), flush=True)
+
+
+def tensor_parallel(args):
+    """N GPUs, one tensor-parallel group: every rank holds 1/N of every layer."""
+    import torch
+    import torch.distributed as dist
+
+    from swarmllm_b200.engine import EngineConfig
+    from swarmllm_b200.models.config import preset
+    from swarmllm_b200.models.weights import RandomSource
+    from swarmllm_b200.parallel.pipeline import init_distributed
+    from swarmllm_b200.parallel.tp_engine import TpEngine
+
+    init_distributed("nccl", timeout_s=600)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cfg = preset(args.model)
+    if args.layers:
+        cfg = cfg.scaled(n_layers=args.layers)
+    B, P, G = args.batch, args.prompt, args.gen
+    chunk = args.chunk or P
+    ecfg = EngineConfig(max_model_len=P + G + 64, max_running=B, max_step_tokens=chunk,
+                        prefill_chunk=chunk, graph_sizes=(1, B))
+    t0 = time.time()
+    eng = TpEngine.create(cfg, ecfg, lambda: RandomSource(cfg, seed=1234, on_device=True))
+    t_init = time.time() - t0
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    replays = []
+    if eng.root:
+        log(f"tp{world} engine ready in {t_init:.1f}s; weights per rank "
+            f"{eng.model.weight_bytes() / 1e9:.1f} GB, kv pages {eng.bm.num_pages}")
+
+        def replay(batch, steps):
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            eng.replay(batch, steps, ev)
+            torch.cuda.synchronize()
+            ms = ev[0].elapsed_time(ev[1])
+            replays.append(ms)
+            return ms
+        inner = eng.runner._inner
+        m = measure(eng, cfg, args, replay, [_visible_gpu(i) for i in range(world)],
+                    lambda: inner.h2d_bytes, lambda: inner.d2h_bytes)
+        eng.stop()
+    else:
+        eng.follow(on_replay=replays.append)
+    # device time: max over ranks of every timed replay
+    t = torch.tensor(replays + [0.0] * (2 - len(replays)), dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=eng.cpu_group)
+    if eng.root:
+        m["ms_b"], m["ms1"] = float(t[0]), float(t[1])
+        line = result_line(cfg, args, m, world, f"tp{world}",
+                           eng.model.weight_bytes() * world / 1e9, eng.model.decode_launches() * world,
+                           {"init_s": round(t_init, 1),
+                            "tp": "row-parallel GEMM epilogue stores each tile into its owner's "
+                                  "buffer over NVLink; fused reduce + residual + RMSNorm + "
+                                  "residual all-gather kernel (P2P stores, epoch flags)"})
+        print(json.dumps(line), flush=True)
+    dist.barrier(group=eng.cpu_group)
+    eng.close()
+    dist.destroy_process_group()
 
 
 def main():
@@ -238,9 +340,12 @@ def main():
     if preset(args.model).n_experts:
         from swarmllm_b200.parallel.bench_ep import ep_bench
         return ep_bench(args)
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    if not args.tp:  # default layout: one tensor-parallel group over all GPUs
+        args.tp = world
+    if args.tp == world and not args.pp_layout:
+        return tensor_parallel(args)
     from swarmllm_b200.parallel.bench_pp import pipeline_bench
-    if not args.tp:  # the headline layouts: PP 2/4 stages, PP4 x TP2 on the 8-GPU runs
-        args.tp = 2 if args.gpus >= 8 else 1
     return pipeline_bench(args)
 
 

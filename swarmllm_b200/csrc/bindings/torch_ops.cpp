@@ -148,7 +148,8 @@ py::tuple dense_tc_plan_py(int64_t rows, int64_t K, int64_t T, int64_t num_sms) 
 GemmResult qgemm_q4k_tc_tp(Tensor w_packed, int64_t rows, int64_t K, Tensor x, Tensor status,
                            int64_t num_sms, int64_t recv_base, int64_t src_stride,
                            std::vector<int64_t> dst_ptrs, Tensor sig_ctl,
-                           std::vector<int64_t> sig_bases, int64_t sig_flag_off, int64_t rank) {
+                           std::vector<int64_t> sig_bases, int64_t sig_flag_off, int64_t rank,
+                           int64_t owner_tiles) {
   CHECK_CUDA(w_packed); CHECK_DT(x, at::kHalf); CHECK_DT(status, at::kInt);
   CHECK_DT(sig_ctl, at::kInt);
   TORCH_CHECK(x.size(-1) == K && x.stride(-1) == 1, "x must be [T, K] with unit inner stride");
@@ -168,11 +169,35 @@ GemmResult qgemm_q4k_tc_tp(Tensor w_packed, int64_t rows, int64_t K, Tensor x, T
                                (int)x.size(0), own, (size_t)src_stride, (int)num_sms,
                                status.data_ptr<int>(), &r.g, cur_stream(), d,
                                (int)dst_ptrs.size(), sig_ctl.data_ptr<int>(), b,
-                               (long long)sig_flag_off, (int)rank);
+                               (long long)sig_flag_off, (int)rank, (int)owner_tiles);
   TORCH_CHECK(rc == 0, "qgemm_q4k_tc_tp launch failed: rc=", rc);
   r.g.n_src = (int)dst_ptrs.size();
   r.g.src_stride = src_stride;
   return r;
+}
+
+// Fused TP reduction of a row-parallel GEMM's owner-routed partials + residual
+// + RMSNorm + residual all-gather (tp_comm.cu).  Offsets are bytes into every
+// rank's arena (same layout on all ranks).
+void tp_reduce_norm(const GemmResult& g, OptT bias, OptT w, OptT out, double eps, int64_t H,
+                    int64_t rank, int64_t T, int64_t t_stride, std::vector<int64_t> bases,
+                    int64_t h_in_off, int64_t h_out_off, int64_t ss_off, int64_t rowflag_off,
+                    int64_t gemm_flags, Tensor ctl, int64_t ctl_gemm_slot, int64_t ctl_row_slot,
+                    Tensor status, int64_t code, int64_t num_sms, int64_t timeout_ns) {
+  CHECK_DT(ctl, at::kInt); CHECK_DT(status, at::kInt);
+  TORCH_CHECK(!bases.empty() && bases.size() <= 8, "1..8 ranks");
+  if (out.has_value()) CHECK_DT(*out, at::kHalf);
+  const at::cuda::CUDAGuard guard(ctl.device());
+  unsigned long long b[8];
+  for (size_t i = 0; i < bases.size(); ++i) b[i] = (unsigned long long)bases[i];
+  int* c = ctl.data_ptr<int>();
+  int rc = launch_tp_reduce_norm(
+      g.g, ptr_or_null<float>(bias), ptr_or_null<float>(w), ptr_or_null<__half>(out),
+      out.has_value() ? (int)out->stride(0) : 0, (float)eps, (int)H, (int)bases.size(), (int)rank,
+      (int)T, (int)t_stride, b, h_in_off, h_out_off, ss_off, rowflag_off,
+      reinterpret_cast<const void*>(gemm_flags), c + ctl_gemm_slot, c + ctl_row_slot,
+      status.data_ptr<int>(), (int)code, (int)num_sms, (long long)timeout_ns, cur_stream());
+  TORCH_CHECK(rc == 0, "tp_reduce_norm launch failed: rc=", rc);
 }
 
 void qgemm_set_trace_py(OptT buf) {
@@ -430,6 +455,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("q4k_gemv_occupancy", [](int64_t T) { return q4k_gemv_occupancy((int)T); });
   m.def("qgemm_q4k_tc", &qgemm_q4k_tc);
   m.def("qgemm_q4k_tc_tp", &qgemm_q4k_tc_tp);
+  m.def("tp_reduce_norm", &tp_reduce_norm);
   m.def("flag_wait", [](int64_t flags, int64_t world, Tensor ctl, int64_t slot, Tensor status,
                         int64_t code) {
     const at::cuda::CUDAGuard guard(ctl.device());

@@ -47,7 +47,7 @@ int launch_qgemv_q4k(const void* w_packed, int rows, int K, const __half* x, int
                      float* ws, int ksb, long total_units, int upc, int ctas, int* status,
                      const unsigned long long* peer_ws, int n_peers, int* sig_ctl,
                      const unsigned long long* sig_bases, long long sig_flag_off, int sig_rank,
-                     cudaStream_t s);
+                     cudaStream_t s, int owner_tiles = 0);
 void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* ksb,
                  long* total_units, int* upc, int* n_ctas, size_t* ws_floats);
 int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, int x_stride,
@@ -55,7 +55,7 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
                         swarm::GemmOut* out, cudaStream_t s,
                         const unsigned long long* peer_ws = nullptr, int n_peers = 0,
                         int* sig_ctl = nullptr, const unsigned long long* sig_bases = nullptr,
-                        long long sig_flag_off = 0, int sig_rank = 0);
+                        long long sig_flag_off = 0, int sig_rank = 0, int owner_tiles = 0);
 void qgemm_set_trace(void* buf);
 // Dense fp16 weights on tcgen05 (dense_gemm_tc.cu); same workspace contract.
 void dense_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* kb,
@@ -163,6 +163,14 @@ int launch_tree_rank(const float* logits, int rows, int V, int stride, int k, fl
                      int* cand_i, float* ms, int S, int32_t* ids, float* logp, cudaStream_t s);
 // Bounded wait (one CTA) until flags[0..world) reach this side's next epoch
 // (ctl[slot] + 1); records code/where in status on timeout.
+// Tensor parallelism (tp_comm.cu): reduce of the owner-routed partials + residual
+// + RMSNorm + all-gather of the residual over peer memory.
+int launch_tp_reduce_norm(const swarm::GemmOut& g, const float* bias, const float* w, __half* out,
+                          int out_stride, float eps, int H, int W, int rank, int T, int t_stride,
+                          const unsigned long long* bases, long long h_in_off, long long h_out_off,
+                          long long ss_off, long long rowflag_off, const void* gemm_flags,
+                          int* ctl_gemm, int* ctl_row, int* status, int code, int num_sms,
+                          long long timeout_ns, cudaStream_t s);
 int launch_flag_wait(const void* flags, int world, int* ctl, int slot, int* status, int code,
                      cudaStream_t s);
 

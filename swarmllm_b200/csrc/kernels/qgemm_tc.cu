@@ -85,6 +85,7 @@ struct QGemmArgs {
   // finishes last raises flag word sig_bases[o] + sig_flag_off + 4 * sig_rank.
   int n_peers;
   unsigned long long peer_ws[8];
+  int owner_tiles;  // > 0: row tile rt goes only to rank rt / owner_tiles (reduce-scatter)
   int* sig_ctl;
   unsigned long long sig_bases[8];
   long long sig_flag_off;
@@ -287,7 +288,10 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
               for (int e = 0; e < 16; ++e)
                 if (c * 16 + e < n_valid) dst[(size_t)(c * 16 + e) * 128] = __uint_as_float(r[e]);
             } else {
-              for (int o = 0; o < a.n_peers; ++o) {
+              const int rt = tile / a.n_tok_tiles;
+              const int o0 = a.owner_tiles > 0 ? rt / a.owner_tiles : 0;
+              const int o1 = a.owner_tiles > 0 ? o0 + 1 : a.n_peers;
+              for (int o = o0; o < o1; ++o) {
                 float* dst = reinterpret_cast<float*>(a.peer_ws[o]) + off;
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
@@ -450,7 +454,7 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
                         int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
                         GemmOut* out, cudaStream_t s, const unsigned long long* peer_ws,
                         int n_peers, int* sig_ctl, const unsigned long long* sig_bases,
-                        long long sig_flag_off, int sig_rank) {
+                        long long sig_flag_off, int sig_rank, int owner_tiles) {
   if (T <= 0) return 0;
   if (K % 256 != 0 || rows % 128 != 0) return -1;
   if ((x_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return -5;
@@ -474,11 +478,13 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
   }
   if (T <= g_gemv_max_t)
     return launch_qgemv_q4k(w_packed, rows, K, x, x_stride, T, ws, kb, total, upc, ctas, status,
-                            peer_ws, n_peers, sig_ctl, sig_bases, sig_flag_off, sig_rank, s);
+                            peer_ws, n_peers, sig_ctl, sig_bases, sig_flag_off, sig_rank, s,
+                            owner_tiles);
   CUtensorMap map;
   if (make_tmap_2d_16bit(&map, x, T, K, x_stride, N, 64, 128) != 0) return -2;
   QGemmArgs a{(const uint8_t*)w_packed, rows, K, T, ntt, kb, total, upc, ws, status, g_trace};
   a.n_peers = 0;
+  a.owner_tiles = 0;
   a.sig_ctl = nullptr;
   if (n_peers > 0) {
     if (n_peers > 8 || !peer_ws || !sig_ctl || !sig_bases) return -7;
@@ -490,6 +496,8 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
     a.sig_ctl = sig_ctl;
     a.sig_flag_off = sig_flag_off;
     a.sig_rank = sig_rank;
+    a.owner_tiles = owner_tiles;
+    if (owner_tiles > 0 && (rows / 128) > owner_tiles * n_peers) return -7;
   }
   switch (N) {
     case 16: return launch_n<16>(map, a, ctas, s);

@@ -67,6 +67,7 @@ struct GemvArgs {
   int* status;
   int n_peers;
   unsigned long long peer_ws[8];
+  int owner_tiles;  // > 0: row tile rt goes only to rank rt / owner_tiles (reduce-scatter)
   int* sig_ctl;
   unsigned long long sig_bases[8];
   long long sig_flag_off;
@@ -218,7 +219,9 @@ __global__ void __launch_bounds__(kGvWarps * 32)
 #pragma unroll
         for (int t = 0; t < T; ++t) a.ws[off + (size_t)t * 128] = acc[t];
       } else {
-        for (int o = 0; o < a.n_peers; ++o) {
+        const int o0 = a.owner_tiles > 0 ? rt / a.owner_tiles : 0;
+        const int o1 = a.owner_tiles > 0 ? o0 + 1 : a.n_peers;
+        for (int o = o0; o < o1; ++o) {
           float* dst = reinterpret_cast<float*>(a.peer_ws[o]) + off;
 #pragma unroll
           for (int t = 0; t < T; ++t) dst[(size_t)t * 128] = acc[t];
@@ -247,15 +250,19 @@ __global__ void __launch_bounds__(kGvWarps * 32)
 // ask for the full shared-memory carveout so they fit.
 template <int T>
 static int setup_t() {
-  static int state = 0;   // 0 unset, 1 ok, <0 error
-  if (state == 0) {
-    state = (cudaFuncSetAttribute(qgemv_q4k_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  GvCfg<T>::SMEM) == cudaSuccess &&
-             cudaFuncSetAttribute(qgemv_q4k_kernel<T>,
-                                  cudaFuncAttributePreferredSharedMemoryCarveout, 100) == cudaSuccess)
-                ? 1 : -3;
-  }
-  return state;
+  // Function attributes apply to the current device: set them once per device.
+  static unsigned long long done = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
+  const unsigned long long bit = 1ull << dev;
+  if (__atomic_load_n(&done, __ATOMIC_ACQUIRE) & bit) return 1;
+  if (cudaFuncSetAttribute(qgemv_q4k_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GvCfg<T>::SMEM) != cudaSuccess ||
+      cudaFuncSetAttribute(qgemv_q4k_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           100) != cudaSuccess)
+    return -3;
+  __atomic_fetch_or(&done, bit, __ATOMIC_RELEASE);
+  return 1;
 }
 
 template <int T>
@@ -291,7 +298,7 @@ int launch_qgemv_q4k(const void* w_packed, int rows, int K, const __half* x, int
                      float* ws, int ksb, long total_units, int upc, int ctas, int* status,
                      const unsigned long long* peer_ws, int n_peers, int* sig_ctl,
                      const unsigned long long* sig_bases, long long sig_flag_off, int sig_rank,
-                     cudaStream_t s) {
+                     cudaStream_t s, int owner_tiles) {
   if (T < 1 || T > kQGemvMaxT) return -1;
   if ((x_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0 ||
       (reinterpret_cast<uintptr_t>(w_packed) & 15) != 0)
@@ -319,6 +326,8 @@ int launch_qgemv_q4k(const void* w_packed, int rows, int K, const __half* x, int
     a.sig_ctl = sig_ctl;
     a.sig_flag_off = sig_flag_off;
     a.sig_rank = sig_rank;
+    a.owner_tiles = owner_tiles;
+    if (owner_tiles > 0 && (rows / 128) > owner_tiles * n_peers) return -7;
   }
   switch (T) {
     case 1: return launch_t<1>(a, ctas, s);

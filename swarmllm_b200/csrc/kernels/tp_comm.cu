@@ -1,0 +1,233 @@
+// Tensor parallelism: the reduction of a row-parallel GEMM (o_proj, down_proj)
+// fused with the residual add, the next RMSNorm and the all-gather of the
+// residual stream, over NVLink peer memory.
+//
+// A layer's row-parallel GEMM on rank r multiplies its K-slice of the weight
+// and produces a partial of the full hidden-wide result.  Its epilogue
+// (qgemm_tc.cu / qgemv_q4k.cu, owner_tiles > 0) stores each 128-column tile
+// of partials only into the receive buffer of the rank that OWNS those hidden
+// columns (rank o owns columns [o*H/W, (o+1)*H/W)): a reduce-scatter done by
+// the GEMM itself, tile by tile, as the tiles come out of TMEM.  Its last CTA
+// raises a "GEMM done" flag in every rank's arena.
+//
+// tp_reduce_norm_kernel, per token row t, on rank r:
+//   1. wait until every rank's GEMM-done flag has reached this call's epoch;
+//   2. for the owned columns: sum the W ranks' partials (GemmOut, n_src = W,
+//      all local reads), add the bias and the residual, store the new residual
+//      into EVERY rank's copy (P2P stores: the all-gather) and publish this
+//      slice's sum of squares next to it, then raise the row flag on every rank;
+//   3. wait for the row flags of all W ranks (local polls), add the W sums of
+//      squares, and normalise the whole row from the local, now complete copy.
+// So each row-parallel layer costs one GEMM launch plus one of this kernel,
+// and every byte that crosses NVLink is a store: a partial tile once to its
+// owner, a residual slice once to each rank.  Nothing is pulled from a peer.
+//
+// Buffers alternate between consecutive calls (parity k % 2 of the call
+// index): partials buffer, residual copy written, sums of squares.  Call k
+// reads the residual from buffer (k+1) % 2 and writes buffer k % 2.  A rank
+// only reaches call k + 2, which overwrites what peers read in call k, after
+// call k + 1 saw every peer's row flags, i.e. after every peer finished call k.
+// Flags carry epochs that every rank counts in lockstep (device counters,
+// advanced by the last CTA of each launch, so CUDA-graph replays advance them
+// too); waits compare with (int)(flag - want) >= 0 and give up after a
+// deadline, recording an error in the status word instead of hanging.
+//
+// Rows are handled by a grid-stride loop in ascending order with at most a
+// few CTAs per SM, so every CTA that waits is resident and the same rows are
+// in flight on every rank.
+//
+// Reference behaviour replaced: the reference's TP sums f32 partials per layer
+// and phase through a star or ring of network messages (src/inference/
+// allreduce.rs:63,413,620) and applies the residual and norm afterwards.
+#include "kernels.h"
+#include "common.cuh"
+#include "ep_common.cuh"
+#include "gemm_out.cuh"
+#include "tc_utils.cuh"
+
+namespace swarm {
+
+struct TpReduceArgs {
+  GemmOut g;                    // this rank's receive buffer, n_src = W sources
+  const float* bias;            // [H] or null (added once, by the column's owner)
+  const float* w;               // RMSNorm weight [H], or null: no normalised output
+  __half* out;                  // [T][out_stride] fp16 normalised rows
+  int out_stride;
+  float eps;
+  int H, W, rank, T, t_stride;  // t_stride: rows of the arena's residual / flag arrays
+  unsigned long long bases[8];  // every rank's arena base (own included)
+  long long h_in_off;           // residual rows read (this rank's copy)
+  long long h_out_off;          // residual rows written into every rank
+  long long ss_off;             // [W][t_stride] fp32 sums of squares (this parity)
+  long long rowflag_off;        // [W][t_stride] u32 row flags
+  const uint32_t* gemm_flags;   // this rank's GEMM-done flags of the receive buffer [W]
+  int* ctl_gemm;                // [0]: last GEMM-done epoch waited for (this buffer)
+  int* ctl_row;                 // [0]: done-CTA counter, [1]: last row epoch
+  int* status;
+  int code;
+  unsigned long long timeout_ns;
+};
+
+SW_DEVICE bool wait_ge(const uint32_t* p, uint32_t want, unsigned long long t0,
+                       unsigned long long timeout_ns) {
+  int n = 0;
+  while ((int)(ld_acquire_sys(p) - want) < 0) {
+    if ((++n & 63) == 0 && tc::globaltimer() - t0 > timeout_ns) return false;
+  }
+  return true;
+}
+
+SW_DEVICE void record_fail(int* status, int code, int d0, int d1, int d2) {
+  if (status && atomicCAS(&status[0], 0, code) == 0) {
+    status[1] = blockIdx.x;
+    status[2] = d0;
+    status[3] = d1;
+    status[4] = d2;
+  }
+}
+
+SW_DEVICE float4 add4(float4 a, float4 b) {
+  return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+__global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const TpReduceArgs a) {
+  __shared__ float red[32];
+  __shared__ int ok_s;
+  const int H = a.H, W = a.W;
+  const uint32_t want_g = (uint32_t)a.ctl_gemm[0] + 1;
+  const uint32_t e = (uint32_t)a.ctl_row[1] + 1;
+  const unsigned long long t0 = tc::globaltimer();
+  if (threadIdx.x == 0) ok_s = 1;
+  __syncthreads();
+  // 1. every rank's partial tiles for our columns have landed
+  if (threadIdx.x < W && !wait_ge(a.gemm_flags + threadIdx.x, want_g, t0, a.timeout_ns)) {
+    ok_s = 0;
+    record_fail(a.status, a.code, threadIdx.x, (int)want_g, -1);
+  }
+  __syncthreads();
+  bool ok = ok_s != 0;
+  const int per = H / W;
+  const int c0 = a.rank * per;
+  const unsigned long long own = a.bases[a.rank];
+  // 2. owned slice of every row this CTA handles: reduce, add, publish
+  if (ok) {
+    for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
+      const float* hin = reinterpret_cast<const float*>(own + a.h_in_off) + (size_t)t * H;
+      float ss = 0.f;
+      for (int i = c0 + 8 * threadIdx.x; i < c0 + per; i += 8 * blockDim.x) {
+        float4 lo, hi;
+        a.g.get8(t, i, lo, hi);
+        lo = add4(lo, *reinterpret_cast<const float4*>(hin + i));
+        hi = add4(hi, *reinterpret_cast<const float4*>(hin + i + 4));
+        if (a.bias) {
+          lo = add4(lo, *reinterpret_cast<const float4*>(a.bias + i));
+          hi = add4(hi, *reinterpret_cast<const float4*>(a.bias + i + 4));
+        }
+        ss += lo.x * lo.x + lo.y * lo.y + lo.z * lo.z + lo.w * lo.w + hi.x * hi.x +
+              hi.y * hi.y + hi.z * hi.z + hi.w * hi.w;
+        for (int o = 0; o < W; ++o) {
+          float* d = reinterpret_cast<float*>(a.bases[o] + a.h_out_off) + (size_t)t * H + i;
+          *reinterpret_cast<float4*>(d) = lo;
+          *reinterpret_cast<float4*>(d + 4) = hi;
+        }
+      }
+      ss = block_sum(ss, red);
+      __threadfence_system();  // this thread's residual stores before the flags below
+      __syncthreads();
+      if (threadIdx.x < W) {
+        const int o = threadIdx.x;
+        reinterpret_cast<float*>(a.bases[o] + a.ss_off)[(size_t)a.rank * a.t_stride + t] = ss;
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<uint32_t*>(a.bases[o] + a.rowflag_off) +
+                           (size_t)a.rank * a.t_stride + t, e);
+      }
+    }
+  }
+  // 3. whole rows: wait for every rank's slice, then normalise
+  for (int t = blockIdx.x; ok && t < a.T; t += gridDim.x) {
+    if (threadIdx.x < W) {
+      const uint32_t* f = reinterpret_cast<const uint32_t*>(own + a.rowflag_off) +
+                          (size_t)threadIdx.x * a.t_stride + t;
+      if (!wait_ge(f, e, t0, a.timeout_ns)) {
+        ok_s = 0;
+        record_fail(a.status, a.code + 1, threadIdx.x, (int)e, t);
+      }
+    }
+    __syncthreads();
+    if (!ok_s) break;
+    if (a.w == nullptr) continue;
+    float tot = 0.f;
+    const float* ssv = reinterpret_cast<const float*>(own + a.ss_off);
+    for (int o = 0; o < W; ++o) tot += __ldcg(ssv + (size_t)o * a.t_stride + t);
+    const float inv = rsqrtf(tot / (float)H + a.eps);
+    const float* h = reinterpret_cast<const float*>(own + a.h_out_off) + (size_t)t * H;
+    __half* o = a.out + (size_t)t * a.out_stride;
+    for (int i = 8 * threadIdx.x; i < H; i += 8 * blockDim.x) {
+      const float4 v0 = __ldcg(reinterpret_cast<const float4*>(h + i));
+      const float4 v1 = __ldcg(reinterpret_cast<const float4*>(h + i + 4));
+      const float4 w0 = *reinterpret_cast<const float4*>(a.w + i);
+      const float4 w1 = *reinterpret_cast<const float4*>(a.w + i + 4);
+      __half2 r[4];
+      r[0] = __floats2half2_rn(v0.x * inv * w0.x, v0.y * inv * w0.y);
+      r[1] = __floats2half2_rn(v0.z * inv * w0.z, v0.w * inv * w0.w);
+      r[2] = __floats2half2_rn(v1.x * inv * w1.x, v1.y * inv * w1.y);
+      r[3] = __floats2half2_rn(v1.z * inv * w1.z, v1.w * inv * w1.w);
+      *reinterpret_cast<uint4*>(o + i) = *reinterpret_cast<const uint4*>(r);
+    }
+  }
+  // the last CTA advances the epochs (every CTA has read them by then)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&a.ctl_row[0], 1);
+    if (prev == (int)gridDim.x - 1) {
+      a.ctl_row[0] = 0;
+      a.ctl_row[1] = (int)e;
+      a.ctl_gemm[0] = (int)want_g;
+    }
+  }
+}
+
+}  // namespace swarm
+
+using namespace swarm;
+
+int launch_tp_reduce_norm(const GemmOut& g, const float* bias, const float* w, __half* out,
+                          int out_stride, float eps, int H, int W, int rank, int T, int t_stride,
+                          const unsigned long long* bases, long long h_in_off, long long h_out_off,
+                          long long ss_off, long long rowflag_off, const void* gemm_flags,
+                          int* ctl_gemm, int* ctl_row, int* status, int code, int num_sms,
+                          long long timeout_ns, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (W < 1 || W > 8 || rank < 0 || rank >= W || T > t_stride) return -1;
+  if (H % (8 * W) != 0 || g.n_src != W || g.rows != H) return -2;
+  if (w && (!out || (out_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(out) & 15) != 0))
+    return -3;
+  TpReduceArgs a{};
+  a.g = g;
+  a.bias = bias;
+  a.w = w;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.eps = eps;
+  a.H = H;
+  a.W = W;
+  a.rank = rank;
+  a.T = T;
+  a.t_stride = t_stride;
+  for (int i = 0; i < W; ++i) a.bases[i] = bases[i];
+  a.h_in_off = h_in_off;
+  a.h_out_off = h_out_off;
+  a.ss_off = ss_off;
+  a.rowflag_off = rowflag_off;
+  a.gemm_flags = static_cast<const uint32_t*>(gemm_flags);
+  a.ctl_gemm = ctl_gemm;
+  a.ctl_row = ctl_row;
+  a.status = status;
+  a.code = code;
+  a.timeout_ns = timeout_ns > 0 ? (unsigned long long)timeout_ns : tc::kWaitTimeoutNs;
+  // at most 2 CTAs per SM: every CTA resident, rows in ascending order on every rank
+  const int grid = T < 2 * num_sms ? T : 2 * num_sms;
+  tp_reduce_norm_kernel<<<grid, 256, 0, s>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}

@@ -290,6 +290,16 @@ class LlamaGPU:
             return lin(x, ctx.gemm)
         return self.tp.row_parallel(lin, x, ctx.gemm.status, ctx.gemm.num_sms)
 
+    def _residual_norm(self, g, h, bias, w, out, ctx):
+        """h += g (+ bias); out = RMSNorm(h) * w (w None: no normalised output).
+        Under TP g holds the owner-routed partials and the sum over ranks, the
+        residual add and the all-gather of h happen in one fused kernel."""
+        eps = self.cfg.rms_eps
+        if self.tp is not None:
+            self.tp.reduce_norm(g, bias, w, out, eps, ctx.gemm.status, ctx.gemm.num_sms)
+        else:
+            C().epi_residual_rmsnorm(g, h, bias, w if w is not None else ctx.dummy_norm, out, eps)
+
     def _deltanet(self, L, b, kv, ctx, x, N):
         """Gated DeltaNet token mixing of one layer -> ctx.ssm_out (fp16)."""
         cfg = self.cfg
@@ -315,8 +325,6 @@ class LlamaGPU:
                 n += 7   # in GEMM, conv, ba GEMM, z GEMM, delta rule, out GEMM, residual+norm
             else:
                 n += 6 + (1 if L.gated else 0)  # qkv GEMM, rope/KV, attention + combine, o GEMM, residual+norm
-            if self.tp is not None:
-                n += 2   # flag waits after the two row-parallel GEMMs
             if L.experts is not None:
                 # router GEMM + top-k, then plan/scatter/2 grouped GEMMs/combine, or under
                 # expert parallelism send-counts/dispatch/wait/plan/2 GEMMs/wait/combine
@@ -374,7 +382,7 @@ class LlamaGPU:
                         C().mul_f16(ao, gate)
                 with P("o_proj+norm"):
                     g = self._lora(j, "o", ao, self._row_parallel(L.wo, ao, ctx), ctx, b)
-                    C().epi_residual_rmsnorm(g, h, L.o_bias, L.ffn_norm, x, cfg.rms_eps)
+                    self._residual_norm(g, h, L.o_bias, L.ffn_norm, x, ctx)
             if j + 1 < len(self.layers):
                 nxt_w, nxt_out = self.layers[j + 1].attn_norm, x
             elif self.last:
@@ -404,8 +412,7 @@ class LlamaGPU:
                 C().epi_swiglu(g, None, self.ffn_loc, 0, False, 0.0, 0.0, act)
             with P("ffn_down+norm"):
                 g = self._lora(j, "down", act, self._row_parallel(L.wdown, act, ctx), ctx, b)
-                C().epi_residual_rmsnorm(g, h, None, nxt_w if nxt_w is not None else ctx.dummy_norm,
-                                         nxt_out, cfg.rms_eps)
+                self._residual_norm(g, h, None, nxt_w, nxt_out, ctx)
         if not self.last:
             return h
         with P("lm_head"):
@@ -455,11 +462,16 @@ class GpuForwardContext:
         self.gemm_side = GemmWorkspace(dev, max_tokens, side_rows, self.gemm.num_sms)
         self.attn = AttentionWorkspace(dev, max_tokens, model.n_q, model.n_kv, cfg.head_dim,
                                        max_len, self.gemm.num_sms)
-        if model.tp is not None:  # receive buffers for the row-parallel (hidden-wide) GEMMs
-            from ..ops.linear import stream_k_floats
-            model.tp.setup(stream_k_floats(max_tokens, cfg.hidden, self.gemm.num_sms))
         H = cfg.hidden
-        self.h = torch.zeros(max_tokens, H, dtype=torch.float32, device=dev)
+        if model.tp is not None:
+            # receive buffers for the row-parallel (hidden-wide) GEMMs; the residual
+            # stream lives in the TP arena, where peers store their slices of it
+            from ..ops.linear import stream_k_floats
+            model.tp.setup(stream_k_floats(max_tokens, cfg.hidden, self.gemm.num_sms), max_tokens, H)
+            self.h = model.tp.h_view()
+            self.h.zero_()
+        else:
+            self.h = torch.zeros(max_tokens, H, dtype=torch.float32, device=dev)
         self.x = torch.zeros(max_tokens, H, dtype=torch.float16, device=dev)
         self.q = torch.zeros(max_tokens, model.n_q, cfg.head_dim, dtype=torch.float16, device=dev)
         self.attn_out = torch.zeros(max_tokens, model.n_q * cfg.head_dim, dtype=torch.float16,

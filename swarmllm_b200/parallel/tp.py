@@ -3,18 +3,36 @@
 Column-parallel layers (q|k|v, gate|up) split their output rows: every rank
 holds n_heads/W query heads, n_kv/W KV heads and ffn/W features, and keeps
 the full (replicated) residual stream, so their input needs no gather.
-Row-parallel layers (o_proj, down_proj) split K; instead of an all-reduce
-call, the Q4_K GEMM's own epilogue pushes its fp32 partial tiles over NVLink
-into every rank's receive buffer (peer stores) and its last CTA raises a flag
-on every rank (qgemm_tc.cu); the residual-add + RMSNorm epilogue then reads
-the sum over the ranks' partials while it reads the GEMM result (GemmOut with
-n_src ranks).  Two receive buffers alternate between consecutive row-parallel
-GEMMs: a rank can only write buffer b again after every rank has read it
-(each rank's next GEMM on b comes after its own wait on the GEMM in between).
+Row-parallel layers (o_proj, down_proj) split K.  Their reduction is fused
+into two kernels over NVLink peer memory, with no collective call:
+
+* the Q4_K GEMM's epilogue stores every 128-column tile of its partial
+  result straight into the receive buffer of the rank that owns those hidden
+  columns (reduce-scatter by P2P stores, tile by tile), and its last CTA
+  raises a "GEMM done" flag on every rank;
+* `tp_reduce_norm` (tp_comm.cu) sums the W partials of the owned columns,
+  adds bias and residual, stores the new residual slice into every rank's
+  copy (all-gather by P2P stores) with its sum of squares, and once every
+  rank's slice of a row is in, applies the next RMSNorm to the whole row.
+
+Per row-parallel layer each rank sends (W-1)/W of its partial result once and
+its residual slice W-1 times; there is no all-gather of partials.
+
+Arena (CUDA-IPC mapped, identical offsets on every rank), in bytes:
+  recv      [2][W][ws]      fp32 partials per source rank (2 alternating buffers)
+  gemm flag [2][W]          u32 GEMM-done epochs, one word per source rank
+  h         [2][t_max][H]   fp32 residual stream copies (call k writes k % 2)
+  ss        [2][W][t_max]   fp32 per-rank sums of squares of each row slice
+  row flag  [W][t_max]      u32 row-slice epochs
+Local control words (int32[16]): [4b+0..2] done counter, signal epoch and
+wait epoch of receive buffer b; [8] done counter and [9] epoch of the rows.
+Between row-parallel calls k and k+1 the residual lives in h[k % 2]; a
+forward makes an even number of calls, so it starts and ends in h[1], which
+`h_view()` exposes as the model's residual stream.
 
 Reference behaviour: the reference's TP splits heads and FFN columns
 (split/executor.rs:3440 pre_split_for_tp) and all-reduces f32 partials over
-the network per layer and phase (R27, src/network tp all-reduce).
+the network per layer and phase (src/inference/allreduce.rs:63,413,620).
 """
 from __future__ import annotations
 
@@ -24,25 +42,44 @@ import torch.distributed as dist
 from ..utils.ext import C
 
 
+class _DevBuf:
+    """Zero-copy torch view of device memory the arena owns."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3}
+
+
 class TpGroup:
-    def __init__(self, rank: int, world: int, device, group=None):
+    # Status codes of the waits (GEMM-done flags, row flags)
+    CODE_REDUCE = 73
+
+    def __init__(self, rank: int, world: int, device, group=None, timeout_ns: int = 0):
         assert 1 <= world <= 8
         self.rank, self.world = rank, world
         self.device = torch.device(device)
         self.group = group
         self.base = None
-        self.buf = 0
+        self.k = 0
+        self.timeout_ns = int(timeout_ns)  # 0: the kernels' default deadline (1 s)
 
-    def setup(self, ws_floats: int):
-        """Allocate this rank's receive buffers and map every peer's (collective)."""
+    def setup(self, ws_floats: int, t_max: int, hidden: int):
+        """Allocate this rank's arena and map every peer's (collective)."""
         if self.base is not None:
-            assert ws_floats <= self.ws_floats
+            assert ws_floats <= self.ws_floats and t_max <= self.t_max and hidden == self.H
             return
         W = self.world
+        assert hidden % (128 * W) == 0, "every rank must own whole 128-column tiles"
+        self.H, self.t_max = int(hidden), int(t_max)
         self.ws_floats = int(ws_floats)
-        self.ws_bytes = (self.ws_floats * 4 + 255) // 256 * 256
+        al = lambda n: (int(n) + 255) // 256 * 256
+        self.ws_bytes = al(self.ws_floats * 4)
         self.flag_off = 2 * W * self.ws_bytes
-        nbytes = self.flag_off + 2 * W * 4 + 256
+        self.h_off = al(self.flag_off + 2 * W * 4)
+        self.h_bytes = self.t_max * self.H * 4
+        self.ss_off = al(self.h_off + 2 * self.h_bytes)
+        self.rf_off = al(self.ss_off + 2 * W * self.t_max * 4)
+        nbytes = al(self.rf_off + W * self.t_max * 4)
         c = C()
         with torch.cuda.device(self.device):
             self.base, handle = c.ep_arena_alloc(nbytes)
@@ -55,22 +92,39 @@ class TpGroup:
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
 
+    def h_view(self) -> torch.Tensor:
+        """The residual stream [t_max, H] fp32 (this rank's copy, buffer 1)."""
+        ptr = self.base + self.h_off + self.h_bytes
+        return torch.as_tensor(_DevBuf(ptr, (self.t_max, self.H)), device=self.device)
+
     def begin_forward(self):
-        self.buf = 0
+        self.k = 0
 
     def row_parallel(self, lin, x: torch.Tensor, status: torch.Tensor, num_sms: int):
-        """GEMM of a K-split Q4_K weight whose result is summed over the group."""
-        b = self.buf
-        self.buf ^= 1
+        """GEMM of a K-split Q4_K weight; each result tile goes to its owner rank."""
+        b = self.k & 1
         W, r = self.world, self.rank
         own = self.base + (b * W) * self.ws_bytes
         dsts = [self.bases[o] + (b * W + r) * self.ws_bytes for o in range(W)]
-        ctl = self.ctl[4 * b:]
-        g = C().qgemm_q4k_tc_tp(lin.packed, lin.rows, lin.K, x, status, num_sms, own,
-                                self.ws_bytes // 4, dsts, ctl, self.bases,
-                                self.flag_off + b * W * 4, r)
-        C().flag_wait(self.base + self.flag_off + b * W * 4, W, ctl, 2, status, 71 + b)
-        return g
+        owner_tiles = self.H // 128 // W
+        return C().qgemm_q4k_tc_tp(lin.packed, lin.rows, lin.K, x, status, num_sms, own,
+                                   self.ws_bytes // 4, dsts, self.ctl[4 * b:], self.bases,
+                                   self.flag_off + b * W * 4, r, owner_tiles)
+
+    def reduce_norm(self, g, bias, w, out, eps: float, status: torch.Tensor, num_sms: int):
+        """Residual += sum over ranks of the row-parallel result (+ bias), then
+        out = RMSNorm(residual) * w; the residual ends up replicated."""
+        k, W = self.k, self.world
+        b = k & 1
+        T = g.T
+        assert T <= self.t_max
+        C().tp_reduce_norm(g, bias, w, out, eps, self.H, self.rank, T, self.t_max, self.bases,
+                           self.h_off + ((k + 1) & 1) * self.h_bytes,
+                           self.h_off + b * self.h_bytes,
+                           self.ss_off + b * W * self.t_max * 4, self.rf_off,
+                           self.base + self.flag_off + b * W * 4, self.ctl, 4 * b + 2, 8,
+                           status, self.CODE_REDUCE, num_sms, self.timeout_ns)
+        self.k += 1
 
     def close(self):
         if self.base is None:

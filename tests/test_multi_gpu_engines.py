@@ -1,0 +1,159 @@
+"""Multi-GPU engines against the single-GPU engine (same random-init weights):
+
+* TpEngine: one tensor-parallel group (TP2, TP4 with 4 GPUs) with the fused
+  owner-routed GEMM epilogue + reduce/RMSNorm/all-gather kernel and CUDA
+  graphs on every rank;
+* AsyncPipelineEngine: wave-pipelined PP2 (and PP2 x TP2 with 4 GPUs) over
+  NCCL p2p.
+
+Greedy tokens must equal the single-GPU engine's (both engines' kernels are
+deterministic; the TP ranks' partial sums only change the order of fp32
+additions).  Skipped with fewer GPUs than ranks."""
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+PROMPT_LENS = (37, 5, 64, 19)
+GEN = 10
+
+
+def _cfg():
+    from swarmllm_b200.models.config import ModelConfig
+    return ModelConfig(name="t", arch="llama", n_layers=4, hidden=1024, n_heads=8, n_kv_heads=4,
+                       head_dim=128, ffn=2048, vocab=2048, weight_qtype="Q4_K",
+                       embed_qtype="F16", output_qtype="Q4_K")
+
+
+def _prompts(cfg):
+    rng = np.random.default_rng(11)
+    return [rng.integers(0, cfg.vocab, n).tolist() for n in PROMPT_LENS]
+
+
+def _ecfg():
+    from swarmllm_b200.engine import EngineConfig
+    return EngineConfig(max_model_len=256, max_running=8, max_step_tokens=256, prefill_chunk=64,
+                        kv_pages=128, graph_sizes=(1, 2, 4, 8), prefix_cache=False)
+
+
+def _reference():
+    """Single-GPU engine: greedy tokens and the first step's logits."""
+    from swarmllm_b200.engine import LLMEngine, SamplingParams
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = _cfg()
+    eng = LLMEngine.from_config(cfg, "cuda:0", _ecfg(), source=RandomSource(cfg, seed=7))
+    outs = eng.generate(_prompts(cfg), SamplingParams(max_tokens=GEN))
+    return [o.token_ids for o in outs]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _init(rank, world, port):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["LOCAL_RANK"] = str(rank)
+    dev = torch.device(f"cuda:{rank}")
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=dev)
+    return dev
+
+
+def _tp_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from swarmllm_b200.engine import SamplingParams
+    from swarmllm_b200.models.weights import RandomSource
+    from swarmllm_b200.parallel.tp_engine import TpEngine
+    _init(rank, world, port)
+    try:
+        cfg = _cfg()
+        eng = TpEngine.create(cfg, _ecfg(), lambda: RandomSource(cfg, seed=7))
+        if eng.root:
+            outs = eng.generate(_prompts(cfg), SamplingParams(max_tokens=GEN))
+            # a second batch through the captured graphs of other sizes
+            outs2 = eng.generate(_prompts(cfg)[:1], SamplingParams(max_tokens=GEN))
+            eng.stop()
+            q.put(([o.token_ids for o in outs], [o.token_ids for o in outs2],
+                   eng.runner._inner.ctx.gemm.status.cpu().tolist()))
+        else:
+            eng.follow()
+            st = eng.runner.ctx.gemm.status.cpu().tolist()
+            assert st[0] == 0, st
+        dist.barrier()
+        eng.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(fn, world, timeout=600):
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=fn, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        got = q.get(timeout=timeout)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return got
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_engine_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    want = _reference()
+    got, got2, status = _spawn(_tp_worker, world)
+    assert status[0] == 0, status
+    assert got == want
+    assert got2 == want[:1]
+
+
+def _pp_worker(rank, world, port, q, tp=1):
+    import torch.distributed as dist
+    from swarmllm_b200.engine import SamplingParams
+    from swarmllm_b200.models.weights import RandomSource
+    from swarmllm_b200.parallel.async_pipeline import AsyncPipelineEngine
+    dev = _init(rank, world, port)
+    try:
+        cfg = _cfg()
+        eng = AsyncPipelineEngine(cfg, _ecfg(), lambda: RandomSource(cfg, seed=7), dev, tp=tp)
+        out = eng.generate(_prompts(cfg), SamplingParams(max_tokens=GEN))
+        if rank == 0:
+            q.put(out)
+        dist.barrier()
+        if eng.tpg is not None:
+            eng.tpg.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _pp_tp2_worker(rank, world, port, q):
+    _pp_worker(rank, world, port, q, tp=2)
+
+
+@pytest.mark.parametrize("world,tp", [(2, 1), (4, 2)])
+def test_async_pipeline_matches_single_gpu(world, tp):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    want = _reference()
+    got = _spawn(_pp_worker if tp == 1 else _pp_tp2_worker, world)
+    assert got == want
