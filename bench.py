@@ -57,6 +57,8 @@ def parse():
                    help="tensor-parallel ranks per pipeline stage (0: all GPUs in one TP group)")
     p.add_argument("--pp-layout", action="store_true",
                    help="run tp == N through the wave-pipelined engine (one stage) instead")
+    p.add_argument("--spec", action="store_true",
+                   help="tree speculative decoding bench (70B target + 1B drafter, one GPU)")
     p.add_argument("--advance", type=int, default=256,
                    help="untimed decode steps before timing (mid-generation context; >= warmup)")
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for the headline)")
@@ -334,6 +336,9 @@ def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.spec:
+        from swarmllm_b200.engine.bench_spec import spec_bench
+        return spec_bench(args, log)
     if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
         return single_gpu(args)
     from swarmllm_b200.models.config import preset

@@ -37,7 +37,18 @@ def _engine(args):
     if loras:
         ecfg.max_loras = max(ecfg.max_loras, len(loras))
     dev = args.device or ("cuda:0" if torch.cuda.is_available() else "cpu")
-    if args.gguf:
+    if getattr(args, "draft_model", None):
+        ecfg.draft_model = args.draft_model
+        ecfg.spec_depth, ecfg.spec_width = args.spec_depth, args.spec_width
+    if ecfg.draft_model:  # speculative serving (drafter preset / GGUF, "self" or "ngram")
+        from .engine.spec_engine import create_engine
+        src = None
+        if args.gguf:
+            from .models.weights import GgufSource
+            src = GgufSource(args.gguf)
+        cfg = src.cfg if src is not None else preset(args.model)
+        eng = create_engine(cfg, dev, ecfg, source=src, seed=args.seed)
+    elif args.gguf:
         eng = LLMEngine.from_gguf(args.gguf, dev, ecfg)
     else:
         eng = LLMEngine.from_config(preset(args.model), dev, ecfg, seed=args.seed)
@@ -112,6 +123,10 @@ def main(argv=None):
         s.add_argument("--lora", action="append", default=[], metavar="NAME=PATH",
                        help="LoRA adapter GGUF; requests select it with model NAME")
         s.add_argument("--mmproj", default=None, help="image encoder GGUF (vision input)")
+        s.add_argument("--draft-model", default="",
+                       help="speculative decoding: drafter preset or GGUF, 'self' or 'ngram'")
+        s.add_argument("--spec-depth", type=int, default=4)
+        s.add_argument("--spec-width", type=int, default=4)
         s.add_argument("--log-file", default=None, help="also log to this file (rotating, 50 MB x 3)")
         s.add_argument("--log-json", action="store_true", help="log one JSON object per line")
         s.add_argument("-v", "--verbose", action="count", default=0)

@@ -50,11 +50,11 @@ void ep_dispatch(Tensor x, Tensor ids, int64_t k, Tensor counts, int64_t E, int6
 }
 
 void ep_wait(int64_t own_base, int64_t world, int64_t cap, int64_t H, int64_t e_loc,
-             int64_t which, Tensor ctl, Tensor status) {
+             int64_t which, Tensor ctl, Tensor status, int64_t timeout_ns) {
   const at::cuda::CUDAGuard guard(ctl.device());
   TORCH_CHECK(launch_ep_wait((unsigned long long)own_base, (int)world, (int)cap, (int)H,
                              (int)e_loc, (int)which, ctl.data_ptr<int>(), status.data_ptr<int>(),
-                             cur_stream()) == 0, "ep_wait launch failed");
+                             cur_stream(), (long long)timeout_ns) == 0, "ep_wait launch failed");
 }
 
 void ep_plan_owner(int64_t own_base, int64_t world, int64_t cap, int64_t H, int64_t e_loc,
@@ -86,6 +86,8 @@ void register_ep_ops(py::module& m) {
   });
   m.def("ep_view", &ep_view);
   m.def("ep_dispatch", &ep_dispatch);
-  m.def("ep_wait", &ep_wait);
+  m.def("ep_wait", &ep_wait, py::arg("own_base"), py::arg("world"), py::arg("cap"), py::arg("H"),
+        py::arg("e_loc"), py::arg("which"), py::arg("ctl"), py::arg("status"),
+        py::arg("timeout_ns") = 0);
   m.def("ep_plan_owner", &ep_plan_owner);
 }

@@ -456,13 +456,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qgemm_q4k_tc", &qgemm_q4k_tc);
   m.def("qgemm_q4k_tc_tp", &qgemm_q4k_tc_tp);
   m.def("tp_reduce_norm", &tp_reduce_norm);
+  // Bounded wait for `world` epoch flags (flags: device address of uint32[world]);
+  // timeout_ns <= 0 uses the kernels' default deadline (1 s).
   m.def("flag_wait", [](int64_t flags, int64_t world, Tensor ctl, int64_t slot, Tensor status,
-                        int64_t code) {
+                        int64_t code, int64_t timeout_ns) {
     const at::cuda::CUDAGuard guard(ctl.device());
     TORCH_CHECK(launch_flag_wait(reinterpret_cast<const void*>(flags), (int)world,
                                  ctl.data_ptr<int>(), (int)slot, status.data_ptr<int>(), (int)code,
-                                 cur_stream()) == 0, "flag_wait launch failed");
-  });
+                                 cur_stream(), (long long)timeout_ns) == 0,
+                "flag_wait launch failed");
+  }, py::arg("flags"), py::arg("world"), py::arg("ctl"), py::arg("slot"), py::arg("status"),
+     py::arg("code"), py::arg("timeout_ns") = 0);
   m.def("q4k_repack", &q4k_repack);
   m.def("dense_gemm_tc", &dense_gemm_tc);
   m.def("dense_tc_plan", &dense_tc_plan_py);

@@ -95,7 +95,8 @@ __global__ void ep_dispatch_kernel(const __half* __restrict__ x, int x_stride, i
 
 // One CTA, `world` threads: wait until flags[src] reaches this side's next epoch.
 __global__ void ep_wait_kernel(const uint32_t* flags, int world, int* __restrict__ ctl,
-                               int wait_slot, int* __restrict__ status, int code) {
+                               int wait_slot, int* __restrict__ status, int code,
+                               unsigned long long timeout_ns) {
   __shared__ int ok_all;
   const uint32_t want = (uint32_t)ctl[wait_slot] + 1;
   if (threadIdx.x == 0) ok_all = 1;
@@ -105,7 +106,7 @@ __global__ void ep_wait_kernel(const uint32_t* flags, int world, int* __restrict
     bool ok = true;
     int n = 0;
     while ((int)(ld_acquire_sys(flags + threadIdx.x) - want) < 0) {
-      if ((++n & 63) == 0 && tc::globaltimer() - t0 > 1000000000ull) {
+      if ((++n & 63) == 0 && tc::globaltimer() - t0 > timeout_ns) {
         ok = false;
         break;
       }
@@ -254,12 +255,14 @@ int launch_ep_dispatch(const __half* x, int x_stride, int H, const int32_t* ids,
 }
 
 int launch_ep_wait(unsigned long long own_base, int world, int cap, int H, int e_loc, int which,
-                   int* ctl, int* status, cudaStream_t s) {
+                   int* ctl, int* status, cudaStream_t s, long long timeout_ns) {
   const EpLayout lay = ep_layout(world, cap, H, e_loc);
   const uint32_t* flags =
       reinterpret_cast<const uint32_t*>(own_base + (which == 0 ? lay.flags_d : lay.flags_c));
   ep_wait_kernel<<<1, 32, 0, s>>>(flags, world, ctl, which == 0 ? 2 : 5, status,
-                                  which == 0 ? 61 : 62);
+                                  which == 0 ? 61 : 62,
+                                  timeout_ns > 0 ? (unsigned long long)timeout_ns
+                                                 : tc::kWaitTimeoutNs);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -277,9 +280,11 @@ int launch_ep_plan_owner(unsigned long long own_base, int world, int cap, int H,
 }
 
 int launch_flag_wait(const void* flags, int world, int* ctl, int slot, int* status, int code,
-                     cudaStream_t s) {
+                     cudaStream_t s, long long timeout_ns) {
   if (world < 1 || world > 32) return -1;
   ep_wait_kernel<<<1, 32, 0, s>>>(reinterpret_cast<const uint32_t*>(flags), world, ctl, slot,
-                                  status, code);
+                                  status, code,
+                                  timeout_ns > 0 ? (unsigned long long)timeout_ns
+                                                 : tc::kWaitTimeoutNs);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }

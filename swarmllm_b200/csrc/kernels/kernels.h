@@ -152,7 +152,7 @@ int launch_ep_dispatch(const __half* x, int x_stride, int H, const int32_t* ids,
                        const unsigned long long* bases, int world, int rank, int x_bf16,
                        int* ctl, cudaStream_t s);
 int launch_ep_wait(unsigned long long own_base, int world, int cap, int H, int e_loc, int which,
-                   int* ctl, int* status, cudaStream_t s);
+                   int* ctl, int* status, cudaStream_t s, long long timeout_ns = 0);
 int launch_ep_plan_owner(unsigned long long own_base, int world, int cap, int H, int e_loc,
                          int tok_tile, void* tiles, int* n_tiles, int max_tiles, int* status,
                          cudaStream_t s);
@@ -172,7 +172,7 @@ int launch_tp_reduce_norm(const swarm::GemmOut& g, const float* bias, const floa
                           int* ctl_gemm, int* ctl_row, int* status, int code, int num_sms,
                           long long timeout_ns, cudaStream_t s);
 int launch_flag_wait(const void* flags, int world, int* ctl, int slot, int* status, int code,
-                     cudaStream_t s);
+                     cudaStream_t s, long long timeout_ns = 0);
 
 // GGML blocks -> fp16 [rows][K] (qmatmul_simt.cu); quantized types only.
 int launch_dequant_f16(const void* w, int type, int rows, int K, __half* out, cudaStream_t s);

@@ -58,6 +58,11 @@ class EngineConfig:
     max_loras: int = 0              # LoRA adapter slots (0: LoRA off)
     state_cache_entries: int = 8    # hybrid models: saved recurrent states for prefix hits
     max_lora_rank: int = 64
+    # speculative serving (engine/spec_engine.py): a drafter preset name, "self"
+    # (the target drafts for itself) or "ngram" (prompt lookup); "" = off
+    draft_model: str = ""
+    spec_depth: int = 4
+    spec_width: int = 4
 
 
 @dataclass

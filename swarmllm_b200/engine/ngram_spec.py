@@ -16,7 +16,10 @@ One round for a batch of sequences:
      sequence is truncated after them
 
 Output equals the target's own greedy decoding.  A sequence with no match
-runs a plain decode step (a chain of one node).
+runs a plain decode step (a chain of one node).  Sampled requests compare the
+chain with the target's coupled samples (Philox noise keyed by seed and
+position, as in engine/spec.py), so their output is what plain sampling
+draws.
 
 Reference behaviour: n-gram lookup speculation (src/inference/ngram_lookup.rs:62,
 model_worker.rs:4131 ngram_spec_round).
@@ -26,9 +29,10 @@ from __future__ import annotations
 import time
 from dataclasses import dataclass, field
 
-import numpy as np
+import numpy as np  # noqa: F401
 
-from .spec import SpecStats, _Side
+from .sampling import DeviceSampler, SamplingParams
+from .spec import SpecStats, _Side, _Seq
 
 
 def ngram_draft(ctx, max_ngram: int, depth: int, min_ngram: int = 1) -> list[int]:
@@ -47,17 +51,8 @@ def ngram_draft(ctx, max_ngram: int, depth: int, min_ngram: int = 1) -> list[int
 
 
 @dataclass
-class _NSeq:
-    sid: int
-    max_new: int
-    ctx: list                       # prompt + committed tokens (the lookup table)
-    out: list = field(default_factory=list)
-    pos: int = 0                    # tokens in the target KV
-    root: int = 0                   # last committed token (not in the KV yet)
-
-    @property
-    def done(self) -> bool:
-        return len(self.out) >= self.max_new
+class _NSeq(_Seq):
+    ctx: list = field(default_factory=list)   # prompt + committed tokens (the lookup table)
 
 
 class NgramSpecDecoder:
@@ -71,8 +66,9 @@ class NgramSpecDecoder:
                        max_model_len + n_nodes + 16, max_seqs)
         self.stats = SpecStats()
         self._next_sid = 0
+        self.t_sampler = DeviceSampler(target.device, max_seqs * n_nodes)
 
-    def add(self, prompt: list[int], max_new: int) -> _NSeq:
+    def add(self, prompt: list[int], max_new: int, params: SamplingParams | None = None) -> _NSeq:
         sid = self._next_sid
         self._next_sid += 1
         side = self.t
@@ -83,9 +79,11 @@ class NgramSpecDecoder:
             c1 = min(len(prompt), c0 + self.chunk)
             rows = [(sid, prompt[i], i, slots[i], i + 1, 0, 0) for i in range(c0, c1)]
             lg = side.forward(rows, [c1 - c0 - 1], tree=False)
-        s = _NSeq(sid, max_new, list(prompt), pos=len(prompt))
-        s.root = int(lg[0].argmax())
-        s.out.append(s.root)
+        s = _NSeq(sid, max_new, pos=len(prompt), ctx=list(prompt))
+        if params is not None:
+            s.params = params
+        s.root = int(self.t_sampler.sample(lg[:1], [s.params], [len(prompt) - 1])[0])
+        s.commit([s.root])
         s.ctx.append(s.root)
         return s
 
@@ -94,7 +92,7 @@ class NgramSpecDecoder:
         if not seqs:
             return
         t0 = time.perf_counter()
-        rows, chains = [], {}
+        rows, chains, rparams = [], {}, []
         for s in seqs:
             room = s.max_new - len(s.out)
             chain = [s.root] + ngram_draft(s.ctx, self.max_ngram, min(self.depth, room))
@@ -102,8 +100,10 @@ class NgramSpecDecoder:
             slots = list(self.t.bm.append_slots(s.sid, n))
             for i, tok in enumerate(chain):
                 rows.append((s.sid, tok, s.pos + i, slots[i], s.pos + n, s.pos, (1 << (i + 1)) - 1))
+                rparams.append(s.params)
             chains[s.sid] = chain
-        tgt = self.t.forward(rows, list(range(len(rows))), tree=True).argmax(-1).cpu().numpy()
+        logits = self.t.forward(rows, list(range(len(rows))), tree=True)
+        tgt = self.t_sampler.sample(logits, rparams, [r[2] for r in rows]).cpu().numpy()
         k0 = 0
         for s in seqs:
             chain = chains[s.sid]
@@ -117,18 +117,21 @@ class NgramSpecDecoder:
             self.t.bm.truncate(s.sid, s.pos + k + 1)
             s.pos += k + 1
             s.root = t[k]
-            room = s.max_new - len(s.out)
-            s.out.extend(new[:room])
-            s.ctx.extend(new[:room])
-            self.stats.committed += min(len(new), room)
+            kept = s.commit(new)
+            s.ctx.extend(new[:kept])
+            self.stats.committed += kept
             self.stats.accepted += k
         self.stats.rounds += 1
         self.stats.seconds += time.perf_counter() - t0
 
-    def generate(self, prompts: list[list[int]], max_new: int) -> list[list[int]]:
-        seqs = [self.add(p, max_new) for p in prompts]
+    def free(self, s: _NSeq):
+        self.t.bm.free_sequence(s.sid)
+
+    def generate(self, prompts: list[list[int]], max_new: int,
+                 params: SamplingParams | None = None) -> list[list[int]]:
+        seqs = [self.add(p, max_new, params) for p in prompts]
         while any(not s.done for s in seqs):
             self.step(seqs)
         for s in seqs:
-            self.t.bm.free_sequence(s.sid)
+            self.free(s)
         return [s.out for s in seqs]

@@ -26,6 +26,17 @@ is the target's argmax given exactly the committed prefix.  With a drafter
 that agrees with the target, each round commits depth + 1 tokens for one
 target forward.
 
+Sampled requests (temperature > 0) use coupled noise: the token for position
+p + 1 is argmax(logits / T + g(seed, p, token)) over the top-k / top-p set,
+with the Gumbel noise g drawn from Philox4x32-10 keyed by (seed, position,
+token) -- the same rule the non-speculative sampler applies.  The target's
+token at every tree node is its coupled sample at that node's position, so a
+committed token is exactly what plain sampling would have drawn after the
+same prefix: acceptance changes the speed, never the output distribution.
+The drafter proposes its own coupled sample at each frontier node (with the
+same seed and positions) as the first child, then its top-k tokens, so a
+drafter whose distribution is close to the target's is accepted often.
+
 Reference: the tree path of the reference's speculative executor (draft trees
 with a visibility bitmask, src/inference/draft_tree.rs:92,617; verify walk,
 src/inference/sampling.rs:496; KV rollback on rejection).
@@ -41,6 +52,8 @@ import torch
 from ..models.llama import StepBatch
 from ..ops.attention import PagedKVCache
 from ..utils.ext import C, native
+from .sampling import DeviceSampler, SamplingParams
+
 
 
 @dataclass
@@ -64,10 +77,24 @@ class _Seq:
     root: int = 0           # last committed token (in neither KV yet)
     dpos: int = 0           # tokens in the drafter KV
     pending: list = field(default_factory=list)  # committed, not yet in the drafter KV
+    params: SamplingParams = field(default_factory=SamplingParams)
+    stopped: bool = False   # end of sequence committed
 
     @property
     def done(self) -> bool:
-        return len(self.out) >= self.max_new
+        return self.stopped or len(self.out) >= self.max_new
+
+    def commit(self, new: list) -> int:
+        """Append committed tokens (up to max_new, through an end-of-sequence
+        token); returns how many were kept."""
+        room = self.max_new - len(self.out)
+        new = new[:room]
+        eos = self.params.eos_token_id
+        if eos >= 0 and not self.params.ignore_eos and eos in new:
+            new = new[:new.index(eos) + 1]
+            self.stopped = True
+        self.out.extend(new)
+        return len(new)
 
 
 class _Side:
@@ -140,6 +167,8 @@ class TreeSpecDecoder:
         self._rk_lp = torch.zeros(rows * width, dtype=torch.float32, device=dev)
         self._rk_ws = torch.zeros(int(C().tree_rank_ws_floats(rows, V, width)),
                                   dtype=torch.float32, device=dev)
+        self.t_sampler = DeviceSampler(target.device, max_seqs * self.n_nodes)
+        self.d_sampler = DeviceSampler(dev, rows + max_seqs)
 
     def _rank(self, logits: torch.Tensor):
         """Top-`width` (log-prob, token) per row on the device (tree_rank kernel)."""
@@ -159,16 +188,35 @@ class TreeSpecDecoder:
             logits = side.forward(rows, [c1 - c0 - 1], tree=False)
         return logits
 
-    def add(self, prompt: list[int], max_new: int) -> _Seq:
+    def add(self, prompt: list[int], max_new: int, params: SamplingParams | None = None) -> _Seq:
         sid = self._next_sid
         self._next_sid += 1
-        s = _Seq(sid, max_new)
+        s = _Seq(sid, max_new, params=params or SamplingParams())
         lg = self._prefill(self.t, sid, prompt)
         self._prefill(self.d, sid, prompt)
-        s.root = int(lg[0].argmax())
-        s.out.append(s.root)
+        s.root = int(self.t_sampler.sample(lg[:1], [s.params], [len(prompt) - 1])[0])
+        s.commit([s.root])
         s.pos = s.dpos = len(prompt)
         return s
+
+    def _proposals(self, logits, seqs_rows: list, positions: list):
+        """Candidate children per drafter row: its top-`width` tokens by
+        log-probability, with the row's coupled sample first for sampled
+        requests (given log-probability 0 so the tree keeps that branch)."""
+        v, ix = self._rank(logits)
+        params = [s.params for s in seqs_rows]
+        if all(p.greedy for p in params):
+            return v, ix
+        samp = self.d_sampler.sample(logits, params, positions).cpu().numpy()
+        W = self.width
+        for r, p in enumerate(params):
+            if p.greedy:
+                continue
+            tok = int(samp[r])
+            rest = [(float(lp), int(t)) for lp, t in zip(v[r], ix[r]) if int(t) != tok][:W - 1]
+            ix[r] = [tok] + [t for _, t in rest]
+            v[r] = [0.0] + [lp for lp, _ in rest]
+        return v, ix
 
     # ------------------------------------------------------------------ one round
     def _draft(self, seqs: list[_Seq]):
@@ -182,14 +230,15 @@ class TreeSpecDecoder:
                 rows.append((s.sid, tok, p, slots[j], p + 1, 0, 0))
             samp.append(len(rows) - 1)
             roots[s.sid] = s.dpos + len(toks) - 1
-        v, ix = self._rank(self.d.forward(rows, samp, tree=False))
+        v, ix = self._proposals(self.d.forward(rows, samp, tree=False), seqs,
+                                [roots[s.sid] for s in seqs])
         trees, fronts = {}, {}
         for n, s in enumerate(seqs):
             tr = native().DraftTree(s.root, self.n_nodes)
             fronts[s.sid] = tr.expand(ix[n].tolist(), v[n].tolist(), W, W)
             trees[s.sid] = tr
         for _ in range(1, D):
-            rows = []
+            rows, owners = [], []
             for s in seqs:
                 tr, fr, r = trees[s.sid], fronts[s.sid], roots[s.sid]
                 slots = list(self.d.bm.append_slots(s.sid, len(fr)))
@@ -197,7 +246,9 @@ class TreeSpecDecoder:
                 for j, node in enumerate(fr):
                     rows.append((s.sid, toks[node], r + deps[node], slots[j], r + len(tr), r,
                                  int(masks[node])))
-            v, ix = self._rank(self.d.forward(rows, list(range(len(rows))), tree=True))
+                    owners.append(s)
+            v, ix = self._proposals(self.d.forward(rows, list(range(len(rows))), tree=True),
+                                    owners, [row[2] for row in rows])
             k0 = 0
             for s in seqs:
                 tr, nf = trees[s.sid], len(fronts[s.sid])
@@ -212,8 +263,9 @@ class TreeSpecDecoder:
             return
         t0 = time.perf_counter()
         trees, droots = self._draft(seqs)
+        self.last_draft_s = time.perf_counter() - t0
         # ---- verify every node with the target
-        rows = []
+        rows, rparams = [], []
         for s in seqs:
             tr = trees[s.sid]
             n = len(tr)
@@ -222,8 +274,10 @@ class TreeSpecDecoder:
             for i in range(n):
                 rows.append((s.sid, toks[i], s.pos + deps[i], slots[i], s.pos + n, s.pos,
                              int(masks[i])))
+                rparams.append(s.params)
         logits = self.t.forward(rows, list(range(len(rows))), tree=True)
-        tgt = logits.argmax(-1).cpu().numpy()
+        # the target's token at every node: argmax, or its coupled sample at that position
+        tgt = self.t_sampler.sample(logits, rparams, [r[2] for r in rows]).cpu().numpy()
         k0 = 0
         for s in seqs:
             tr = trees[s.sid]
@@ -242,18 +296,20 @@ class TreeSpecDecoder:
             s.pending = [toks[i] for i in path[keep:]]
             s.pos += len(path)
             s.root = bonus
-            room = s.max_new - len(s.out)
-            s.out.extend(new[:room])
-            self.stats.committed += min(len(new), room)
+            self.stats.committed += s.commit(new)
             self.stats.accepted += len(path) - 1
         self.stats.rounds += 1
         self.stats.seconds += time.perf_counter() - t0
 
-    def generate(self, prompts: list[list[int]], max_new: int) -> list[list[int]]:
-        seqs = [self.add(p, max_new) for p in prompts]
+    def free(self, s: _Seq):
+        self.t.bm.free_sequence(s.sid)
+        self.d.bm.free_sequence(s.sid)
+
+    def generate(self, prompts: list[list[int]], max_new: int,
+                 params: SamplingParams | None = None) -> list[list[int]]:
+        seqs = [self.add(p, max_new, params) for p in prompts]
         while any(not s.done for s in seqs):
             self.step(seqs)
         for s in seqs:
-            self.t.bm.free_sequence(s.sid)
-            self.d.bm.free_sequence(s.sid)
+            self.free(s)
         return [s.out for s in seqs]

@@ -11,6 +11,10 @@ overrides.  Names kept where the meaning matches:
   max_seq_len_override            -> EngineConfig.max_model_len
   prefix_cache_enabled            -> EngineConfig.prefix_cache
   cuda_graphs (SWARMLLM_CUDA_GRAPH=0 disables)
+  draft_model_path                -> EngineConfig.draft_model (speculative serving; also a
+                                     preset name, "self" or "ngram")
+  speculative_gamma = 4           -> EngineConfig.spec_depth (draft tree depth)
+  speculative_width = 4           -> EngineConfig.spec_width (children kept per level)
 
 Environment: SWARMLLM_MAX_MODEL_LEN, SWARMLLM_MAX_RUNNING, SWARMLLM_PREFILL_CHUNK,
 SWARMLLM_KV_PAGES, SWARMLLM_KV_FRACTION, SWARMLLM_PREFIX_CACHE, SWARMLLM_CUDA_GRAPH.
@@ -38,6 +42,9 @@ _TOML_KEYS = {
     "kv_fraction": "kv_fraction",
     "cuda_graphs": "cuda_graphs",
     "page_size": "page_size",
+    "draft_model_path": "draft_model",      # drafter GGUF (or preset / "self" / "ngram")
+    "speculative_gamma": "spec_depth",      # draft depth (tokens guessed per round)
+    "speculative_width": "spec_width",
 }
 
 _ENV = {
@@ -49,6 +56,9 @@ _ENV = {
     "SWARMLLM_KV_FRACTION": ("kv_fraction", float),
     "SWARMLLM_PREFIX_CACHE": ("prefix_cache", lambda v: v not in ("0", "false", "False")),
     "SWARMLLM_CUDA_GRAPH": ("cuda_graphs", lambda v: v not in ("0", "false", "False")),
+    "SWARMLLM_DRAFT_MODEL": ("draft_model", str),
+    "SWARMLLM_SPEC_DEPTH": ("spec_depth", int),
+    "SWARMLLM_SPEC_WIDTH": ("spec_width", int),
 }
 
 
