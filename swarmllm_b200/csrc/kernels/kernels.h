@@ -165,6 +165,7 @@ int launch_tree_rank(const float* logits, int rows, int V, int stride, int k, fl
 // (ctl[slot] + 1); records code/where in status on timeout.
 // Tensor parallelism (tp_comm.cu): reduce of the owner-routed partials + residual
 // + RMSNorm + all-gather of the residual over peer memory.
+int tp_reduce_slices(int T, int H, int W, int num_sms);  // CTAs per row of tp_reduce_norm
 int launch_tp_reduce_norm(const swarm::GemmOut& g, const float* bias, const float* w, __half* out,
                           int out_stride, float eps, int H, int W, int rank, int T, int t_stride,
                           const unsigned long long* bases, long long h_in_off, long long h_out_off,

@@ -18,6 +18,9 @@
 //      slice's sum of squares next to it, then raise the row flag on every rank;
 //   3. wait for the row flags of all W ranks (local polls), add the W sums of
 //      squares, and normalise the whole row from the local, now complete copy.
+// A row is split into C slices handled by C CTAs (C up to 16 for a few rows,
+// 1 for prefill chunks), so decode spreads the partial sums over many SMs;
+// flags and sums of squares are then per (rank, slice).
 // So each row-parallel layer costs one GEMM launch plus one of this kernel,
 // and every byte that crosses NVLink is a store: a partial tile once to its
 // owner, a residual slice once to each rank.  Nothing is pulled from a peer.
@@ -55,11 +58,12 @@ struct TpReduceArgs {
   int out_stride;
   float eps;
   int H, W, rank, T, t_stride;  // t_stride: rows of the arena's residual / flag arrays
+  int C;                        // CTAs per row: each owns 1/C of the rank's columns
   unsigned long long bases[8];  // every rank's arena base (own included)
   long long h_in_off;           // residual rows read (this rank's copy)
   long long h_out_off;          // residual rows written into every rank
-  long long ss_off;             // [W][t_stride] fp32 sums of squares (this parity)
-  long long rowflag_off;        // [W][t_stride] u32 row flags
+  long long ss_off;             // [W*C][t_stride] fp32 slice sums of squares (this parity)
+  long long rowflag_off;        // [W*C][t_stride] u32 slice flags
   const uint32_t* gemm_flags;   // this rank's GEMM-done flags of the receive buffer [W]
   int* ctl_gemm;                // [0]: last GEMM-done epoch waited for (this buffer)
   int* ctl_row;                 // [0]: done-CTA counter, [1]: last row epoch
@@ -90,10 +94,12 @@ SW_DEVICE float4 add4(float4 a, float4 b) {
   return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
 }
 
+// Work unit u = t * C + j: slice j of row t.  Phase 2 (reduce + publish) covers
+// the rank's own columns of the slice, phase 3 (normalise) 1/C of the whole row.
 __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const TpReduceArgs a) {
   __shared__ float red[32];
   __shared__ int ok_s;
-  const int H = a.H, W = a.W;
+  const int H = a.H, W = a.W, C = a.C;
   const uint32_t want_g = (uint32_t)a.ctl_gemm[0] + 1;
   const uint32_t e = (uint32_t)a.ctl_row[1] + 1;
   const unsigned long long t0 = tc::globaltimer();
@@ -105,13 +111,15 @@ __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const TpReduceArgs 
     record_fail(a.status, a.code, threadIdx.x, (int)want_g, -1);
   }
   __syncthreads();
-  bool ok = ok_s != 0;
-  const int per = H / W;
-  const int c0 = a.rank * per;
+  const bool ok = ok_s != 0;
+  const int per = H / (W * C);              // owned columns of one slice
   const unsigned long long own = a.bases[a.rank];
-  // 2. owned slice of every row this CTA handles: reduce, add, publish
+  const int units = a.T * C;
+  // 2. owned columns of every slice this CTA handles: reduce, add, publish
   if (ok) {
-    for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int t = u / C, j = u - t * C;
+      const int c0 = (a.rank * C + j) * per;
       const float* hin = reinterpret_cast<const float*>(own + a.h_in_off) + (size_t)t * H;
       float ss = 0.f;
       for (int i = c0 + 8 * threadIdx.x; i < c0 + per; i += 8 * blockDim.x) {
@@ -136,33 +144,38 @@ __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const TpReduceArgs 
       __syncthreads();
       if (threadIdx.x < W) {
         const int o = threadIdx.x;
-        reinterpret_cast<float*>(a.bases[o] + a.ss_off)[(size_t)a.rank * a.t_stride + t] = ss;
+        const size_t slot = (size_t)(a.rank * C + j) * a.t_stride + t;
+        reinterpret_cast<float*>(a.bases[o] + a.ss_off)[slot] = ss;
         __threadfence_system();
-        st_release_sys(reinterpret_cast<uint32_t*>(a.bases[o] + a.rowflag_off) +
-                           (size_t)a.rank * a.t_stride + t, e);
+        st_release_sys(reinterpret_cast<uint32_t*>(a.bases[o] + a.rowflag_off) + slot, e);
       }
     }
   }
-  // 3. whole rows: wait for every rank's slice, then normalise
-  for (int t = blockIdx.x; ok && t < a.T; t += gridDim.x) {
-    if (threadIdx.x < W) {
-      const uint32_t* f = reinterpret_cast<const uint32_t*>(own + a.rowflag_off) +
-                          (size_t)threadIdx.x * a.t_stride + t;
-      if (!wait_ge(f, e, t0, a.timeout_ns)) {
+  // 3. 1/C of each whole row: wait for every slice of every rank, then normalise
+  const int nflags = W * C;
+  const int hc = H / C;
+  for (int u = blockIdx.x; ok && u < units; u += gridDim.x) {
+    const int t = u / C, j = u - t * C;
+    for (int f = threadIdx.x; f < nflags; f += blockDim.x) {
+      const uint32_t* p = reinterpret_cast<const uint32_t*>(own + a.rowflag_off) +
+                          (size_t)f * a.t_stride + t;
+      if (!wait_ge(p, e, t0, a.timeout_ns)) {
         ok_s = 0;
-        record_fail(a.status, a.code + 1, threadIdx.x, (int)e, t);
+        record_fail(a.status, a.code + 1, f, (int)e, t);
       }
     }
     __syncthreads();
     if (!ok_s) break;
     if (a.w == nullptr) continue;
-    float tot = 0.f;
     const float* ssv = reinterpret_cast<const float*>(own + a.ss_off);
-    for (int o = 0; o < W; ++o) tot += __ldcg(ssv + (size_t)o * a.t_stride + t);
+    float part = 0.f;
+    for (int f = threadIdx.x; f < nflags; f += blockDim.x)
+      part += __ldcg(ssv + (size_t)f * a.t_stride + t);
+    const float tot = block_sum(part, red);
     const float inv = rsqrtf(tot / (float)H + a.eps);
     const float* h = reinterpret_cast<const float*>(own + a.h_out_off) + (size_t)t * H;
     __half* o = a.out + (size_t)t * a.out_stride;
-    for (int i = 8 * threadIdx.x; i < H; i += 8 * blockDim.x) {
+    for (int i = j * hc + 8 * threadIdx.x; i < (j + 1) * hc; i += 8 * blockDim.x) {
       const float4 v0 = __ldcg(reinterpret_cast<const float4*>(h + i));
       const float4 v1 = __ldcg(reinterpret_cast<const float4*>(h + i + 4));
       const float4 w0 = *reinterpret_cast<const float4*>(a.w + i);
@@ -192,6 +205,14 @@ __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const TpReduceArgs 
 
 using namespace swarm;
 
+int tp_reduce_slices(int T, int H, int W, int num_sms) {
+  // CTAs per row: fill about two CTAs per SM, each slice a whole number of
+  // 8-column groups of the rank's columns
+  int c = 1;
+  while (c < 16 && T * (2 * c) <= 2 * num_sms && (H / W) % (8 * 2 * c) == 0) c *= 2;
+  return c;
+}
+
 int launch_tp_reduce_norm(const GemmOut& g, const float* bias, const float* w, __half* out,
                           int out_stride, float eps, int H, int W, int rank, int T, int t_stride,
                           const unsigned long long* bases, long long h_in_off, long long h_out_off,
@@ -201,6 +222,7 @@ int launch_tp_reduce_norm(const GemmOut& g, const float* bias, const float* w, _
   if (T <= 0) return 0;
   if (W < 1 || W > 8 || rank < 0 || rank >= W || T > t_stride) return -1;
   if (H % (8 * W) != 0 || g.n_src != W || g.rows != H) return -2;
+  const int C = tp_reduce_slices(T, H, W, num_sms);
   if (w && (!out || (out_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(out) & 15) != 0))
     return -3;
   TpReduceArgs a{};
@@ -215,6 +237,7 @@ int launch_tp_reduce_norm(const GemmOut& g, const float* bias, const float* w, _
   a.rank = rank;
   a.T = T;
   a.t_stride = t_stride;
+  a.C = C;
   for (int i = 0; i < W; ++i) a.bases[i] = bases[i];
   a.h_in_off = h_in_off;
   a.h_out_off = h_out_off;
@@ -227,7 +250,8 @@ int launch_tp_reduce_norm(const GemmOut& g, const float* bias, const float* w, _
   a.code = code;
   a.timeout_ns = timeout_ns > 0 ? (unsigned long long)timeout_ns : tc::kWaitTimeoutNs;
   // at most 2 CTAs per SM: every CTA resident, rows in ascending order on every rank
-  const int grid = T < 2 * num_sms ? T : 2 * num_sms;
+  const int units = T * C;
+  const int grid = units < 2 * num_sms ? units : 2 * num_sms;
   tp_reduce_norm_kernel<<<grid, 256, 0, s>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

@@ -288,9 +288,11 @@ class AsyncPipelineEngine:
         self._flush()
 
     # ------------------------------------------------------------------ collective API
-    def run(self, on_events=None, stop_when=None):
+    def run(self, on_events=None, stop_when=None, on_step=None):
         """Collective: every rank calls it.  The root drives until no wave has
-        work (or `stop_when()` is true) and passes events to on_events."""
+        work (or `stop_when()` is true) and passes events to on_events.
+        `on_step()` runs on every rank after each wave step it handled (the
+        failover layer heartbeats there; an exception it raises ends run)."""
         if self.root:
             inflight, busy = deque(), [False] * self.V
             draining = False
@@ -300,6 +302,8 @@ class AsyncPipelineEngine:
                 ev = self._root_round(inflight, busy, issue=not draining)
                 if on_events and ev:
                     on_events(ev)
+                if on_step is not None:
+                    on_step()
                 if not inflight and (draining or not any(s.has_work() for s in self.scheds)):
                     break
             self._stop()
@@ -316,6 +320,8 @@ class AsyncPipelineEngine:
                 self._flush()
                 return
             self._stage_step(hdr, body, h_in)
+            if on_step is not None:
+                on_step()
 
     def generate(self, prompts, params: SamplingParams | None = None):
         """Collective; the root returns the generated tokens per prompt."""

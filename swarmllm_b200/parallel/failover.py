@@ -90,8 +90,10 @@ class ResilientPipeline:
     def __init__(self, build_engine, rank: int, world: int, ctl_host: str, ctl_port: int,
                  backend: str = "gloo", pg_timeout_s: float = 10.0, grace_s: float | None = None,
                  heartbeat_stale_s: float = 30.0, outliers: OutlierTracker | None = None):
-        """`build_engine()` returns a PipelineEngine over the current default
-        process group; it is called again after every re-plan."""
+        """`build_engine()` returns a pipeline engine over the current default
+        process group -- the synchronous PipelineEngine (collective step()) or
+        the wave-pipelined AsyncPipelineEngine (collective run()); it is called
+        again after every re-plan."""
         self.rank, self.world0 = rank, world
         self.backend, self.pg_timeout_s = backend, pg_timeout_s
         # a survivor that only learns of the failure from the group timeout
@@ -180,11 +182,14 @@ class ResilientPipeline:
                             continue
                         sp = SamplingParams(**{**r.params.__dict__, "max_tokens": left})
                         rid_of[self.eng.add_request(r.prompt + r.out, sp)] = i
-                while self.eng.has_work():
-                    for rid, tok, fin in self.eng.step():
+                def take(events):
+                    for rid, tok, fin in events:
                         r = reqs[rid_of[rid]]
                         r.out.append(tok)
                         r.done = r.done or fin
+
+                def beat():
+                    nonlocal step
                     step += 1
                     self._heartbeat(step)
                     if self.root:
@@ -192,6 +197,12 @@ class ResilientPipeline:
                         if stale:
                             self._suspects = stale
                             raise RankFailure(f"stale heartbeat: {stale}")
+                if hasattr(self.eng, "run"):   # wave-pipelined engine: one collective run
+                    self.eng.run(on_events=take if self.root else None, on_step=beat)
+                else:
+                    while self.eng.has_work():
+                        take(self.eng.step())
+                        beat()
                 return [r.out for r in reqs] if self.root else None
             except (RuntimeError, dist.DistBackendError):
                 if self.recoveries >= max_recoveries:

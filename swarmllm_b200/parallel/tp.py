@@ -22,8 +22,8 @@ Arena (CUDA-IPC mapped, identical offsets on every rank), in bytes:
   recv      [2][W][ws]      fp32 partials per source rank (2 alternating buffers)
   gemm flag [2][W]          u32 GEMM-done epochs, one word per source rank
   h         [2][t_max][H]   fp32 residual stream copies (call k writes k % 2)
-  ss        [2][W][t_max]   fp32 per-rank sums of squares of each row slice
-  row flag  [W][t_max]      u32 row-slice epochs
+  ss        [2][W*16][t_max] fp32 sums of squares per (rank, row slice)
+  row flag  [W*16][t_max]   u32 epochs per (rank, row slice)
 Local control words (int32[16]): [4b+0..2] done counter, signal epoch and
 wait epoch of receive buffer b; [8] done counter and [9] epoch of the rows.
 Between row-parallel calls k and k+1 the residual lives in h[k % 2]; a
@@ -51,8 +51,9 @@ class _DevBuf:
 
 
 class TpGroup:
-    # Status codes of the waits (GEMM-done flags, row flags)
+    # Status codes of the waits (GEMM-done flags; +1: row-slice flags)
     CODE_REDUCE = 73
+    MAX_SLICES = 16  # CTAs per row of tp_reduce_norm (tp_comm.cu tp_reduce_slices)
 
     def __init__(self, rank: int, world: int, device, group=None, timeout_ns: int = 0):
         assert 1 <= world <= 8
@@ -78,8 +79,9 @@ class TpGroup:
         self.h_off = al(self.flag_off + 2 * W * 4)
         self.h_bytes = self.t_max * self.H * 4
         self.ss_off = al(self.h_off + 2 * self.h_bytes)
-        self.rf_off = al(self.ss_off + 2 * W * self.t_max * 4)
-        nbytes = al(self.rf_off + W * self.t_max * 4)
+        self.slots = W * self.MAX_SLICES
+        self.rf_off = al(self.ss_off + 2 * self.slots * self.t_max * 4)
+        nbytes = al(self.rf_off + self.slots * self.t_max * 4)
         c = C()
         with torch.cuda.device(self.device):
             self.base, handle = c.ep_arena_alloc(nbytes)
@@ -121,7 +123,7 @@ class TpGroup:
         C().tp_reduce_norm(g, bias, w, out, eps, self.H, self.rank, T, self.t_max, self.bases,
                            self.h_off + ((k + 1) & 1) * self.h_bytes,
                            self.h_off + b * self.h_bytes,
-                           self.ss_off + b * W * self.t_max * 4, self.rf_off,
+                           self.ss_off + b * self.slots * self.t_max * 4, self.rf_off,
                            self.base + self.flag_off + b * W * 4, self.ctl, 4 * b + 2, 8,
                            status, self.CODE_REDUCE, num_sms, self.timeout_ns)
         self.k += 1

@@ -1,5 +1,5 @@
-"""Failure recovery of the pipeline engine on CPU ranks (gloo): a stage's
-process dies mid-generation; the survivors re-plan the layers over the
+"""Failure recovery of the pipeline engines (synchronous and wave-pipelined)
+on CPU ranks (gloo): a stage's process dies mid-generation; the survivors re-plan the layers over the
 remaining ranks, replay the unfinished requests, and the output equals an
 undisturbed single-process run.  The failure is made on the host (a rank
 exits); no GPU is involved."""
@@ -29,7 +29,7 @@ def _prompts():
     return [rng.integers(0, 32000, n).tolist() for n in (12, 7, 20)]
 
 
-def _worker(rank, world, port, ctl_port, crash_rank, crash_after, q):
+def _worker(rank, world, port, ctl_port, crash_rank, crash_after, q, waves=False):
     import torch
     torch.set_num_threads(1)
     from swarmllm_b200.engine.engine import EngineConfig
@@ -44,6 +44,23 @@ def _worker(rank, world, port, ctl_port, crash_rank, crash_after, q):
                         prefix_cache=False, cuda_graphs=False)
 
     def build():
+        if waves:
+            from swarmllm_b200.parallel.async_pipeline import AsyncPipelineEngine
+            eng = AsyncPipelineEngine(cfg, ecfg, lambda: RandomSource(cfg, seed=5), "cpu")
+            if rank == crash_rank:
+                steps = {"n": 0}
+                real_run = eng.run
+
+                def run(on_events=None, stop_when=None, on_step=None):
+                    def hook():
+                        steps["n"] += 1
+                        if steps["n"] > crash_after:
+                            os._exit(17)  # the process dies between its wave steps
+                        if on_step is not None:
+                            on_step()
+                    return real_run(on_events, stop_when, hook)
+                eng.run = run
+            return eng
         eng = PipelineEngine(cfg, ecfg, lambda: RandomSource(cfg, seed=5), "cpu")
         if rank == crash_rank:
             steps = {"n": 0}
@@ -67,7 +84,12 @@ def _worker(rank, world, port, ctl_port, crash_rank, crash_after, q):
     rp.close()
 
 
-def test_stage_failure_replans_and_replays():
+def _waves_worker(rank, world, port, ctl_port, crash_rank, crash_after, q):
+    _worker(rank, world, port, ctl_port, crash_rank, crash_after, q, waves=True)
+
+
+@pytest.mark.parametrize("waves", [False, True])
+def test_stage_failure_replans_and_replays(waves):
     from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
     from swarmllm_b200.models.weights import RandomSource
     cfg = _cfg()
@@ -80,7 +102,8 @@ def test_stage_failure_replans_and_replays():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port, ctl = _free_port(), _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 3, port, ctl, 2, 4, q)) for r in range(3)]
+    fn = _waves_worker if waves else _worker
+    procs = [ctx.Process(target=fn, args=(r, 3, port, ctl, 2, 4, q)) for r in range(3)]
     for p in procs:
         p.start()
     try:
