@@ -23,13 +23,14 @@ void rmsnorm(Tensor x, Tensor w, Tensor out, double eps) {
 }
 
 void epi_residual_rmsnorm(const GemmResult& g, Tensor residual, OptT bias, Tensor w, OptT out,
-                          double eps) {
+                          double eps, OptT post_w) {
   CHECK_DT(residual, at::kFloat);
   TORCH_CHECK(residual.size(-1) == g.g.rows, "residual width != GEMM rows");
   const at::cuda::CUDAGuard guard(residual.device());
   launch_epi_residual_rmsnorm(g.g, residual.data_ptr<float>(), ptr_or_null<float>(bias),
                               w.data_ptr<float>(), ptr_or_null<__half>(out), (float)eps,
-                              out.has_value() ? (int)out->stride(0) : 0, cur_stream());
+                              out.has_value() ? (int)out->stride(0) : 0, cur_stream(),
+                              ptr_or_null<float>(post_w));
 }
 
 void epi_rope_kv(const GemmResult& g, OptT bias, Tensor positions, OptT slots, Tensor inv_freq,
@@ -337,7 +338,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def_readonly("ws", &GemmResult::ws);
   m.def("embed_gather", &embed_gather);
   m.def("rmsnorm", &rmsnorm);
-  m.def("epi_residual_rmsnorm", &epi_residual_rmsnorm);
+  m.def("epi_residual_rmsnorm", &epi_residual_rmsnorm, py::arg("g"), py::arg("residual"),
+        py::arg("bias"), py::arg("w"), py::arg("out"), py::arg("eps"),
+        py::arg("post_w") = py::none());
   m.def("epi_rope_kv", &epi_rope_kv, py::arg("g"), py::arg("bias"), py::arg("positions"),
         py::arg("slots"), py::arg("inv_freq"), py::arg("n_q"), py::arg("n_kv"),
         py::arg("head_dim"), py::arg("rope_dim"), py::arg("neox"), py::arg("attn_factor"),

@@ -66,7 +66,9 @@ __global__ void __launch_bounds__(128) decode_attn_split_kernel(DecodeAttnArgs a
   const uint64_t tmask = a.tree_mask ? a.tree_mask[t] : ~0ull;
   const int tstart = a.tree_start ? a.tree_start[t] : 0x7fffffff;
   const int nk = k_end - k_begin;
-  constexpr int PER_LANE = D / 32;  // dims per lane
+  // dims per lane: D / 32 for D = 64, 128, 256; 4 for D = 96 (lanes 24..31 idle)
+  constexpr int PER_LANE = (D % 64 == 0) ? D / 32 : 4;
+  const bool lane_on = lane * PER_LANE < D;
   // Phase 1: scores.  A warp takes one key at a time: coalesced 2*D-byte row.
   for (int j = warp; j < nk; j += 4) {
     const int key = k_begin + j;
@@ -75,8 +77,8 @@ __global__ void __launch_bounds__(128) decode_attn_split_kernel(DecodeAttnArgs a
     float kf[PER_LANE];
 #pragma unroll
     for (int e = 0; e < PER_LANE; e += 2) {
-      __half2 h2 = *reinterpret_cast<const __half2*>(kr + lane * PER_LANE + e);
-      float2 f = __half22float2(h2);
+      float2 f = make_float2(0.f, 0.f);
+      if (lane_on) f = __half22float2(*reinterpret_cast<const __half2*>(kr + lane * PER_LANE + e));
       kf[e] = f.x;
       kf[e + 1] = f.y;
     }
@@ -85,8 +87,10 @@ __global__ void __launch_bounds__(128) decode_attn_split_kernel(DecodeAttnArgs a
 #pragma unroll
     for (int h = 0; h < NREP; ++h) {
       float p = 0.f;
+      if (lane_on) {
 #pragma unroll
-      for (int e = 0; e < PER_LANE; ++e) p = fmaf(qs[h * D + lane * PER_LANE + e], kf[e], p);
+        for (int e = 0; e < PER_LANE; ++e) p = fmaf(qs[h * D + lane * PER_LANE + e], kf[e], p);
+      }
       p = warp_sum(p);
       if (a.softcap > 0.f) p = a.softcap * tanhf(p / a.softcap);
       if (lane == 0) sc[h * a.keys_per_split + j] = vis ? p : -INFINITY;
@@ -204,6 +208,7 @@ int launch_decode_attn_simt(const __half* q, const __half* k_cache, const __half
   int rc;
   switch (head_dim) {
     case 64: rc = dispatch_nrep<64>(a, nrep, T, s); break;
+    case 96: rc = dispatch_nrep<96>(a, nrep, T, s); break;
     case 128: rc = dispatch_nrep<128>(a, nrep, T, s); break;
     case 256: rc = dispatch_nrep<256>(a, nrep, T, s); break;
     default: return -1;

@@ -135,6 +135,44 @@ __global__ void epi_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ resid
     o[i] = __float2half_rn(row[i] * inv * w[i]);
 }
 
+// Sandwich-norm variant (Gemma 2/3, GLM-4): the branch output is normalised
+// before it joins the residual stream.
+//   v = RMSNorm(g + bias) * post_w;  residual += v;  out = RMSNorm(residual) * w
+// One CTA per token, the row staged in shared memory.
+template <int kThreads>
+__global__ void epi_postnorm_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ residual,
+                                                     const float* __restrict__ bias,
+                                                     const float* __restrict__ post_w,
+                                                     const float* __restrict__ w,
+                                                     __half* __restrict__ out, float eps,
+                                                     int out_stride) {
+  extern __shared__ float row[];
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const int dim = g.rows;
+  float* rr = residual + (size_t)t * dim;
+  float ssg = 0.f;
+  for (int i = threadIdx.x; i < dim; i += kThreads) {
+    const float v = g.get(t, i) + (bias ? bias[i] : 0.f);
+    row[i] = v;
+    ssg += v * v;
+  }
+  ssg = block_sum(ssg, red);
+  const float invg = rsqrtf(ssg / dim + eps);
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < dim; i += kThreads) {
+    const float v = rr[i] + row[i] * invg * post_w[i];
+    rr[i] = v;
+    row[i] = v;
+    ss += v * v;
+  }
+  if (out == nullptr) return;
+  ss = block_sum(ss, red);
+  const float inv = rsqrtf(ss / dim + eps);
+  __half* o = out + (size_t)t * out_stride;
+  for (int i = threadIdx.x; i < dim; i += kThreads) o[i] = __float2half_rn(row[i] * inv * w[i]);
+}
+
 // Grid (token, group of kRopeHpb heads) over the head list [q | k | v].
 // Layout of the QKV GEMM rows: [q heads][k heads][v heads], each head_dim
 // wide -- or, for gated attention, each q head as [q | gate].
@@ -300,9 +338,16 @@ __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
   }
 }
 
+// GELU with the tanh approximation (Hendrycks & Gimpel 2016): the Gemma FFN.
+SW_DEVICE float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
+  return 0.5f * x * (1.f + tanhf(k0 * (x + 0.044715f * x * x * x)));
+}
+
 // rows [0, F) are gate, [F, 2F) are up (or interleaved for gpt-oss: even=gate,
 // odd=up when `interleaved`).  kind 0: silu(g)*u.  kind 1: gpt-oss clamped
 // SwiGLU x=min(g,limit), u=clamp(u,-limit,limit), x*sigmoid(alpha*x)*(u+1).
+// kind 2: gelu_tanh(g)*u (GeGLU).
 __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int F, int kind,
                                   int interleaved, float alpha, float limit,
                                   __half* __restrict__ out) {
@@ -322,6 +367,8 @@ __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int
         float uv = us[e] + (bias ? bias[F + i + e] : 0.f);
         if (kind == 0) {
           y[e] = __float2half_rn(__fdividef(gv, 1.f + __expf(-gv)) * uv);
+        } else if (kind == 2) {
+          y[e] = __float2half_rn(gelu_tanh(gv) * uv);
         } else {
           gv = fminf(gv, limit);
           uv = fminf(fmaxf(uv, -limit), limit);
@@ -344,6 +391,8 @@ __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int
         float uv = us[e] + (bias ? bias[F + i + e] : 0.f);
         if (kind == 0) {
           y[e] = __float2half_rn(silu(gv) * uv);
+        } else if (kind == 2) {
+          y[e] = __float2half_rn(gelu_tanh(gv) * uv);
         } else {
           gv = fminf(gv, limit);
           uv = fminf(fmaxf(uv, -limit), limit);
@@ -362,6 +411,8 @@ __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int
     float y;
     if (kind == 0) {
       y = silu(gv) * uv;
+    } else if (kind == 2) {
+      y = gelu_tanh(gv) * uv;
     } else {
       gv = fminf(gv, limit);
       uv = fminf(fmaxf(uv, -limit), limit);
@@ -463,8 +514,18 @@ __global__ void __launch_bounds__(256) epi_residual_rmsnorm_cluster_kernel(
 
 void launch_epi_residual_rmsnorm(const GemmOut& g, float* residual, const float* bias,
                                  const float* w, __half* out, float eps, int out_stride,
-                                 cudaStream_t s) {
+                                 cudaStream_t s, const float* post_w) {
   if (g.T <= 0) return;
+  if (post_w != nullptr) {
+    const size_t sm = (size_t)g.rows * sizeof(float);
+    if (sm > 48 * 1024)
+      cudaFuncSetAttribute(epi_postnorm_residual_rmsnorm_kernel<512>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    epi_postnorm_residual_rmsnorm_kernel<512><<<g.T, 512, sm, s>>>(
+        g, residual, bias, post_w, w, out, eps, out_stride ? out_stride : g.rows);
+    SW_LAUNCH_CHECK();
+    return;
+  }
   if (g.T < 64) {
     const int per = (g.rows + kClusterNorm - 1) / kClusterNorm;
     cudaLaunchConfig_t cfg = {};

@@ -20,7 +20,7 @@ void launch_rmsnorm(const float* x, const float* w, __half* out, int rows, int d
                     cudaStream_t s);
 void launch_epi_residual_rmsnorm(const swarm::GemmOut& g, float* residual, const float* bias,
                                  const float* w, __half* out, float eps, int out_stride,
-                                 cudaStream_t s);
+                                 cudaStream_t s, const float* post_w = nullptr);
 void launch_epi_rope_kv(const swarm::GemmOut& g, const float* bias, const int32_t* positions,
                         const int32_t* slots, const float* inv_freq, int n_q, int n_kv,
                         int head_dim, int rope_dim, int neox, float attn_factor, __half* q_out,

@@ -12,6 +12,28 @@ mapping in ``src/inference/split/loader/mod.rs``):
 * ``qwen3next`` hybrid: gated DeltaNet linear-attention layers and gated full
                 attention layers (3:1), q/k RMSNorm, partial NEOX RoPE,
                 512-expert MoE with a shared expert.
+
+The other families are the dense / MoE decoder with options, read from the
+GGUF architecture name (llama.cpp's names and metadata keys):
+
+* ``mistral``   Llama layout.
+* ``qwen2``     q/k/v biases, NEOX RoPE (Qwen2 / Qwen2.5).
+* ``qwen3``     per-head q/k RMSNorm, NEOX RoPE.
+* ``qwen2moe``  Qwen2 attention; softmax over all experts, top-k without
+                renormalisation, sigmoid-gated shared expert.
+* ``qwen3moe``  Qwen3 attention; top-k then softmax over the selected experts.
+* ``gemma``     GELU(tanh)-gated FFN, embeddings scaled by sqrt(hidden), tied
+                output, NEOX RoPE.
+* ``gemma2``    Gemma plus post-attention / post-FFN norms on each branch,
+                attention-logit and final-logit soft-capping, a sliding window
+                on every other layer.
+* ``gemma3``    Gemma 2's layout with q/k RMSNorm, no soft-capping, five
+                windowed layers to each global one, and RoPE base 10000 on the
+                windowed layers.
+* ``phi3``      fused q|k|v and gate|up tensors, NEOX RoPE, optional
+                LongRoPE per-dimension factors.
+* ``glm4``      fused q|k|v with biases, fused gate|up, partial interleaved
+                RoPE, post-attention / post-FFN norms.
 """
 from __future__ import annotations
 
@@ -44,6 +66,18 @@ class ModelConfig:
     sliding_window: int = 0
     swa_every: int = 0                  # layer l uses SWA if swa_every and l % swa_every == 0
     attn_output_gate: bool = False      # qwen3next gated attention
+    attn_out_bias: bool | None = None   # output-projection bias (None: same as attn_bias)
+    act: str = "silu"                   # gated-FFN activation: "silu" | "gelu" (tanh approximation)
+    embed_scale: float = 0.0            # token embeddings times this (0: none; gemma sqrt(hidden))
+    attn_softcap: float = 0.0           # attention logits c * tanh(s / c) (gemma2)
+    final_softcap: float = 0.0          # output logits c * tanh(l / c) (gemma2)
+    post_norms: bool = False            # RMSNorm of each branch output before the residual add
+    swa_pattern: int = 0                # layer l windowed iff (l + 1) % swa_pattern != 0 (gemma3)
+    rope_local_theta: float = 0.0       # RoPE base of the windowed layers (gemma3), 0: same
+    attn_scale: float = 0.0             # softmax scale (0: 1 / sqrt(head_dim))
+    fused_qkv: bool = False             # file layout: one attn_qkv tensor (phi3, glm4)
+    fused_gate_up: bool = False         # file layout: ffn_up holds gate | up (phi3, glm4)
+    rope_factors: list | None = None    # LongRoPE per-pair frequency divisors (phi3)
     # MoE
     n_experts: int = 0
     n_experts_used: int = 0
@@ -77,7 +111,19 @@ class ModelConfig:
         return self.rope_dim or self.head_dim
 
     def is_swa(self, layer: int) -> bool:
-        return bool(self.sliding_window and self.swa_every and layer % self.swa_every == 0)
+        if not self.sliding_window:
+            return False
+        if self.swa_pattern:
+            return (layer + 1) % self.swa_pattern != 0
+        return bool(self.swa_every and layer % self.swa_every == 0)
+
+    @property
+    def has_out_bias(self) -> bool:
+        return self.attn_bias if self.attn_out_bias is None else self.attn_out_bias
+
+    @property
+    def softmax_scale(self) -> float:
+        return self.attn_scale or 1.0 / math.sqrt(self.head_dim)
 
     def is_linear_attn(self, layer: int) -> bool:
         return bool(self.full_attn_interval) and (layer + 1) % self.full_attn_interval != 0
@@ -103,16 +149,27 @@ class ModelConfig:
         return L * (attn + ffn) + emb
 
 
-def rope_inv_freq(cfg: ModelConfig) -> tuple[np.ndarray, float]:
+def rope_inv_freq(cfg: ModelConfig, local: bool = False) -> tuple[np.ndarray, float]:
     """Per-pair inverse frequencies (length rot_dim/2) and the cos/sin
-    attention factor, including llama3 / linear / YaRN scaling.  The scaling
-    rules are the published ones (Meta's llama3 rope_scaling; YaRN, Peng et
-    al. 2023); the reference implements the same in src/inference/split/rope.rs:66-249."""
+    attention factor, including llama3 / linear / YaRN / LongRoPE scaling.
+    The scaling rules are the published ones (Meta's llama3 rope_scaling;
+    YaRN, Peng et al. 2023; LongRoPE, Ding et al. 2024); the reference
+    implements the same in src/inference/split/rope.rs:66-249.  `local`: the
+    windowed layers of a model with a separate local base (gemma3), which
+    take no scaling."""
     d = cfg.rot_dim
-    inv = 1.0 / (cfg.rope_theta ** (np.arange(0, d, 2, dtype=np.float64) / d))
+    theta = cfg.rope_local_theta if (local and cfg.rope_local_theta) else cfg.rope_theta
+    inv = 1.0 / (theta ** (np.arange(0, d, 2, dtype=np.float64) / d))
     factor_attn = 1.0
-    rs = cfg.rope_scaling or {}
+    rs = {} if (local and cfg.rope_local_theta) else (cfg.rope_scaling or {})
     t = rs.get("type")
+    if cfg.rope_factors is not None and not (local and cfg.rope_local_theta):
+        inv = inv / np.asarray(cfg.rope_factors, np.float64)[: d // 2]
+        if t == "longrope":
+            scale = rs.get("factor", 1.0)
+            old = rs.get("original_max_position_embeddings", 4096)
+            factor_attn = rs.get("attn_factor") or (
+                math.sqrt(1 + math.log(scale) / math.log(old)) if scale > 1 else 1.0)
     if t == "linear":
         inv = inv / rs["factor"]
     elif t == "llama3":
@@ -225,7 +282,43 @@ def preset(name: str) -> ModelConfig:
 
 
 # --------------------------------------------------------------------------- GGUF mapping
-_ARCH_KEYS = {"llama": "llama", "gpt-oss": "gpt-oss", "qwen3next": "qwen3next"}
+_FAMILIES = ("llama", "mistral", "qwen2", "qwen3", "qwen2moe", "qwen3moe", "gemma", "gemma2",
+             "gemma3", "phi3", "glm4", "gpt-oss", "qwen3next")
+_ARCH_KEYS = {f: f for f in _FAMILIES}    # GGUF general.architecture == family name
+
+
+def apply_family(cfg: ModelConfig, md: dict | None = None) -> ModelConfig:
+    """Set the options a family implies (and those its GGUF metadata carries)."""
+    fam = cfg.arch
+    g = (lambda k, d=None: md.get(f"{fam}.{k}", d)) if md is not None else (lambda k, d=None: d)
+    if fam in ("qwen2", "qwen2moe"):
+        cfg.rope_neox, cfg.attn_bias, cfg.attn_out_bias = True, True, False
+    if fam in ("qwen3", "qwen3moe"):
+        cfg.rope_neox, cfg.qk_norm = True, True
+    if fam == "qwen2moe":
+        cfg.moe_softmax_after_topk = False      # softmax over all experts, no renormalisation
+    if fam in ("gemma", "gemma2", "gemma3"):
+        cfg.rope_neox, cfg.act, cfg.tie_embeddings = True, "gelu", True
+        cfg.embed_scale = math.sqrt(cfg.hidden)
+    if fam == "gemma2":
+        cfg.post_norms, cfg.swa_every = True, 2
+        cfg.attn_softcap = float(g("attn_logit_softcapping", cfg.attn_softcap or 50.0))
+        cfg.final_softcap = float(g("final_logit_softcapping", cfg.final_softcap or 30.0))
+    if fam == "gemma3":
+        cfg.post_norms, cfg.qk_norm, cfg.swa_pattern = True, True, 6
+        cfg.rope_local_theta = cfg.rope_local_theta or 10000.0
+    if fam == "phi3":
+        cfg.rope_neox, cfg.fused_qkv, cfg.fused_gate_up = True, True, True
+    if fam == "glm4":
+        cfg.fused_qkv, cfg.fused_gate_up, cfg.post_norms = True, True, True
+        cfg.attn_bias, cfg.attn_out_bias = True, False
+        cfg.rope_dim = cfg.rope_dim or cfg.head_dim // 2
+    if fam == "gpt-oss":
+        cfg.rope_neox, cfg.attn_sinks, cfg.attn_bias, cfg.swa_every = True, True, True, 2
+        cfg.swiglu_limit = cfg.swiglu_limit or 7.0
+    if fam == "qwen3next":
+        cfg.rope_neox, cfg.qk_norm, cfg.attn_output_gate = True, True, True
+    return cfg
 
 
 def to_gguf_metadata(cfg: ModelConfig) -> dict:
@@ -258,6 +351,10 @@ def to_gguf_metadata(cfg: ModelConfig) -> dict:
             md[f"{a}.expert_shared_feed_forward_length"] = cfg.shared_expert_ffn
     if cfg.sliding_window:
         md[f"{a}.attention.sliding_window"] = cfg.sliding_window
+    if cfg.attn_softcap:
+        md[f"{a}.attn_logit_softcapping"] = float(cfg.attn_softcap)
+    if cfg.final_softcap:
+        md[f"{a}.final_logit_softcapping"] = float(cfg.final_softcap)
     if cfg.full_attn_interval:
         md[f"{a}.full_attention_interval"] = cfg.full_attn_interval
         md[f"{a}.ssm.conv_kernel"] = cfg.ssm_conv_kernel
@@ -274,7 +371,7 @@ def from_gguf_metadata(md: dict) -> ModelConfig:
     if "swarmllm.config" in md:
         return ModelConfig(**json.loads(md["swarmllm.config"]))
     arch = md["general.architecture"]
-    fam = {"llama": "llama", "gpt-oss": "gpt-oss", "qwen3next": "qwen3next"}.get(arch)
+    fam = arch if arch in _FAMILIES else None
     if fam is None:
         raise ValueError(f"unsupported architecture {arch}")
     a = arch
@@ -299,14 +396,16 @@ def from_gguf_metadata(md: dict) -> ModelConfig:
         cfg.shared_expert_ffn = g("expert_shared_feed_forward_length", 0)
     if g("attention.sliding_window"):
         cfg.sliding_window = g("attention.sliding_window")
-    if g("rope.scaling.type") in ("linear", "yarn"):
-        cfg.rope_scaling = {"type": g("rope.scaling.type"), "factor": g("rope.scaling.factor"),
+    if g("rope.scaling.type") in ("linear", "yarn", "longrope"):
+        cfg.rope_scaling = {"type": g("rope.scaling.type"), "factor": g("rope.scaling.factor", 1.0),
                             "original_max_position_embeddings": g("rope.scaling.original_context_length", 4096)}
-    if fam == "gpt-oss":
-        cfg.rope_neox, cfg.attn_sinks, cfg.attn_bias, cfg.swa_every = True, True, True, 2
-        cfg.swiglu_limit = 7.0
+        if g("rope.scaling.attn_factor"):
+            cfg.rope_scaling["attn_factor"] = g("rope.scaling.attn_factor")
+    if g("attention.scale"):
+        cfg.attn_scale = float(g("attention.scale"))
     if fam == "qwen3next":
-        cfg.rope_neox, cfg.qk_norm, cfg.attn_output_gate = True, True, True
         cfg.full_attn_interval = g("full_attention_interval", 4)
         cfg.ssm_conv_kernel = g("ssm.conv_kernel", 4)
-    return cfg
+    if fam in ("gemma", "gemma2", "gemma3") and not g("vocab_size"):
+        cfg.vocab = len(md.get("tokenizer.ggml.tokens", [])) or cfg.vocab
+    return apply_family(cfg, md)

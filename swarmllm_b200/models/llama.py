@@ -118,28 +118,42 @@ class LlamaGPU:
             else:
                 L.kv_idx = n_attn
                 n_attn += 1
-                parts = [get(b + n) for n in ("attn_q.weight", "attn_k.weight", "attn_v.weight")]
-                qt = parts[0][1]
-                assert all(p[1] == qt for p in parts), "q/k/v must share a quant type"
                 d = cfg.head_dim
                 qh = 2 * d if cfg.attn_output_gate else d
                 shares = ((tr * self.n_q * qh, (tr + 1) * self.n_q * qh),
                           (tr * self.n_kv * d, (tr + 1) * self.n_kv * d),
                           (tr * self.n_kv * d, (tr + 1) * self.n_kv * d))
-                pieces = [split_rows(p[0], qt, p[2], a, z) if W > 1 else p[0]
-                          for p, (a, z) in zip(parts, shares)]
                 rows = sum(z - a for a, z in shares)
-                L.wqkv = QLinear(torch.cat(pieces), qt, rows, H, dev)
-                L.qkv_bias = None
-                if cfg.attn_bias:
-                    L.qkv_bias = torch.cat([small(b + n)[a:z] for n, (a, z) in
-                                            zip(("attn_q.bias", "attn_k.bias", "attn_v.bias"),
-                                                shares)])
+                if cfg.fused_qkv:  # one q|k|v tensor: each part's rows at its offset
+                    t, qt, shape = get(b + "attn_qkv.weight")
+                    base = (0, cfg.n_heads * qh, cfg.n_heads * qh + cfg.kv_dim)
+                    if W > 1:
+                        t = torch.cat([split_rows(t, qt, shape, o + a, o + z)
+                                       for o, (a, z) in zip(base, shares)])
+                    L.wqkv = QLinear(t, qt, rows, H, dev)
+                    L.qkv_bias = None
+                    if cfg.attn_bias:
+                        bq = small(b + "attn_qkv.bias")
+                        L.qkv_bias = torch.cat([bq[o + a:o + z] for o, (a, z) in zip(base, shares)])
+                else:
+                    parts = [get(b + n) for n in ("attn_q.weight", "attn_k.weight", "attn_v.weight")]
+                    qt = parts[0][1]
+                    assert all(p[1] == qt for p in parts), "q/k/v must share a quant type"
+                    pieces = [split_rows(p[0], qt, p[2], a, z) if W > 1 else p[0]
+                              for p, (a, z) in zip(parts, shares)]
+                    L.wqkv = QLinear(torch.cat(pieces), qt, rows, H, dev)
+                    L.qkv_bias = None
+                    if cfg.attn_bias:
+                        L.qkv_bias = torch.cat([small(b + n)[a:z] for n, (a, z) in
+                                                zip(("attn_q.bias", "attn_k.bias", "attn_v.bias"),
+                                                    shares)])
                 t, qt, shape = get(b + "attn_output.weight")
                 if W > 1:
                     t = split_cols(t, qt, shape, tr * self.n_q * d, (tr + 1) * self.n_q * d)
                 L.wo = QLinear(t, qt, shape[0], self.n_q * d, dev)
-                L.o_bias = small(b + "attn_output.bias") if cfg.attn_bias else None
+                L.o_bias = small(b + "attn_output.bias") if cfg.has_out_bias else None
+                L.post_attn_norm = small(b + "post_attention_norm.weight") if cfg.post_norms else None
+                L.local_rope = bool(cfg.rope_local_theta) and cfg.is_swa(i)
                 L.q_norm = small(b + "attn_q_norm.weight") if cfg.qk_norm else None
                 L.k_norm = small(b + "attn_k_norm.weight") if cfg.qk_norm else None
                 L.sinks = (small(b + "attn_sinks.weight")[tr * self.n_q:(tr + 1) * self.n_q]
@@ -147,14 +161,21 @@ class LlamaGPU:
                 L.window = cfg.sliding_window if cfg.is_swa(i) else 0
                 L.gated = cfg.attn_output_gate
             L.experts = None
+            L.post_ffn_norm = small(b + "post_ffw_norm.weight") if cfg.post_norms else None
             if cfg.n_experts:
                 self._load_moe(L, b, get, small)
             else:
-                g, u = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
                 F = self.ffn_loc
-                if W > 1:
-                    gp = split_rows(g[0], g[1], g[2], tr * F, (tr + 1) * F)
-                    up = split_rows(u[0], u[1], u[2], tr * F, (tr + 1) * F)
+                if cfg.fused_gate_up:  # ffn_up holds gate rows [0, ffn) then up rows [ffn, 2 ffn)
+                    u = get(b + "ffn_up.weight")
+                    g = u
+                    goff, uoff = 0, cfg.ffn
+                else:
+                    g, u = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
+                    goff = uoff = 0
+                if W > 1 or cfg.fused_gate_up:
+                    gp = split_rows(g[0], g[1], g[2], goff + tr * F, goff + (tr + 1) * F)
+                    up = split_rows(u[0], u[1], u[2], uoff + tr * F, uoff + (tr + 1) * F)
                 else:
                     gp, up = g[0], u[0]
                 L.wgu = QLinear(torch.cat([gp, up]), g[1], 2 * F, H, dev)
@@ -175,7 +196,12 @@ class LlamaGPU:
             self.head = QLinear(t, qt, shape[0], shape[1], dev)
         inv, self.attn_factor = rope_inv_freq(cfg)
         self.inv_freq = torch.from_numpy(inv).to(dev)
-        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        inv_l, self.attn_factor_local = rope_inv_freq(cfg, local=True)
+        self.inv_freq_local = torch.from_numpy(inv_l).to(dev)
+        self.scale = cfg.softmax_scale
+        self.act_kind = 2 if cfg.act == "gelu" else 0
+        if tp is not None:
+            assert not cfg.post_norms, "tensor parallelism covers the pre-norm families"
 
     def _load_deltanet(self, L, b, get, small):
         """Gated DeltaNet layer: in-projection (q|k|v), z gate, beta/decay
@@ -290,15 +316,17 @@ class LlamaGPU:
             return lin(x, ctx.gemm)
         return self.tp.row_parallel(lin, x, ctx.gemm.status, ctx.gemm.num_sms)
 
-    def _residual_norm(self, g, h, bias, w, out, ctx):
+    def _residual_norm(self, g, h, bias, w, out, ctx, post_w=None):
         """h += g (+ bias); out = RMSNorm(h) * w (w None: no normalised output).
+        `post_w`: the branch output is RMSNorm-ed with it before the add.
         Under TP g holds the owner-routed partials and the sum over ranks, the
         residual add and the all-gather of h happen in one fused kernel."""
         eps = self.cfg.rms_eps
         if self.tp is not None:
             self.tp.reduce_norm(g, bias, w, out, eps, ctx.gemm.status, ctx.gemm.num_sms)
         else:
-            C().epi_residual_rmsnorm(g, h, bias, w if w is not None else ctx.dummy_norm, out, eps)
+            C().epi_residual_rmsnorm(g, h, bias, w if w is not None else ctx.dummy_norm, out, eps,
+                                     post_w)
 
     def _deltanet(self, L, b, kv, ctx, x, N):
         """Gated DeltaNet token mixing of one layer -> ctx.ssm_out (fp16)."""
@@ -348,6 +376,8 @@ class LlamaGPU:
         h = ctx.h[:N]
         if self.first:
             C().embed_gather(self.embd, self.embd_type, H, b.tokens, h)
+            if cfg.embed_scale:
+                h.mul_(cfg.embed_scale)
             if b.embed_rows is not None:  # image rows spliced into the prompt
                 h.index_copy_(0, b.embed_rows.long(), b.embed_vals.to(h.dtype))
         elif h_in is not None and h_in.data_ptr() != h.data_ptr():
@@ -370,19 +400,22 @@ class LlamaGPU:
                 with P("qkv_proj+rope+kv_append"):
                     g = self._lora(j, "qkv", x, L.wqkv(x, ctx.gemm), ctx, b)
                     gate = ctx.gate[:N] if L.gated else None
-                    C().epi_rope_kv(g, L.qkv_bias, b.positions, b.slots, self.inv_freq, nq, nkv, d,
-                                    cfg.rot_dim, cfg.rope_neox, self.attn_factor, q, kv.k(li),
+                    inv, af = ((self.inv_freq_local, self.attn_factor_local) if L.local_rope
+                               else (self.inv_freq, self.attn_factor))
+                    C().epi_rope_kv(g, L.qkv_bias, b.positions, b.slots, inv, nq, nkv, d,
+                                    cfg.rot_dim, cfg.rope_neox, af, q, kv.k(li),
                                     kv.v(li), kv.page_size, L.q_norm, L.k_norm, cfg.rms_eps, gate)
                 with P("attention"):
                     paged_attention(q, kv.k(li), kv.v(li), b.block_table, b.seq_lens, ctx.attn,
                                     ao.view(N, nq, d), b.max_len, self.scale, L.window, L.sinks,
+                                    softcap=cfg.attn_softcap,
                                     tree_mask=b.tree_mask, tree_start=b.tree_start,
                                     num_sms=ctx.gemm.num_sms, groups=b.groups)
                     if gate is not None:
                         C().mul_f16(ao, gate)
                 with P("o_proj+norm"):
                     g = self._lora(j, "o", ao, self._row_parallel(L.wo, ao, ctx), ctx, b)
-                    self._residual_norm(g, h, L.o_bias, L.ffn_norm, x, ctx)
+                    self._residual_norm(g, h, L.o_bias, L.ffn_norm, x, ctx, L.post_attn_norm)
             if j + 1 < len(self.layers):
                 nxt_w, nxt_out = self.layers[j + 1].attn_norm, x
             elif self.last:
@@ -409,10 +442,10 @@ class LlamaGPU:
                 continue
             with P("ffn_gate_up+act"):
                 g = self._lora(j, "gu", x, L.wgu(x, ctx.gemm), ctx, b)
-                C().epi_swiglu(g, None, self.ffn_loc, 0, False, 0.0, 0.0, act)
+                C().epi_swiglu(g, None, self.ffn_loc, self.act_kind, False, 0.0, 0.0, act)
             with P("ffn_down+norm"):
                 g = self._lora(j, "down", act, self._row_parallel(L.wdown, act, ctx), ctx, b)
-                self._residual_norm(g, h, None, nxt_w, nxt_out, ctx)
+                self._residual_norm(g, h, None, nxt_w, nxt_out, ctx, L.post_ffn_norm)
         if not self.last:
             return h
         with P("lm_head"):
@@ -422,6 +455,8 @@ class LlamaGPU:
             g = self.head(xs, ctx.gemm)
             logits = ctx.logits[:S]
             C().epi_copy(g, None, logits)
+            if cfg.final_softcap:  # c * tanh(logits / c)
+                logits.div_(cfg.final_softcap).tanh_().mul_(cfg.final_softcap)
         return logits
 
     def _stage_ctx(self):
@@ -550,12 +585,25 @@ class LlamaCPU:
                 continue
             L.kv_idx = n_attn
             n_attn += 1
-            L.wq, L.wk, L.wv = dq(b + "attn_q.weight"), dq(b + "attn_k.weight"), dq(b + "attn_v.weight")
+            qr = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
+            if cfg.fused_qkv:
+                wqkv = dq(b + "attn_qkv.weight")
+                L.wq, L.wk, L.wv = wqkv[:qr], wqkv[qr:qr + cfg.kv_dim], wqkv[qr + cfg.kv_dim:]
+                if cfg.attn_bias:
+                    bqkv = dq(b + "attn_qkv.bias")
+                    L.bq, L.bk, L.bv = bqkv[:qr], bqkv[qr:qr + cfg.kv_dim], bqkv[qr + cfg.kv_dim:]
+                else:
+                    L.bq = L.bk = L.bv = None
+            else:
+                L.wq, L.wk, L.wv = dq(b + "attn_q.weight"), dq(b + "attn_k.weight"), dq(b + "attn_v.weight")
+                L.bq = dq(b + "attn_q.bias") if cfg.attn_bias else None
+                L.bk = dq(b + "attn_k.bias") if cfg.attn_bias else None
+                L.bv = dq(b + "attn_v.bias") if cfg.attn_bias else None
             L.wo = dq(b + "attn_output.weight")
-            L.bq = dq(b + "attn_q.bias") if cfg.attn_bias else None
-            L.bk = dq(b + "attn_k.bias") if cfg.attn_bias else None
-            L.bv = dq(b + "attn_v.bias") if cfg.attn_bias else None
-            L.bo = dq(b + "attn_output.bias") if cfg.attn_bias else None
+            L.bo = dq(b + "attn_output.bias") if cfg.has_out_bias else None
+            L.post_attn = dq(b + "post_attention_norm.weight") if cfg.post_norms else None
+            L.post_ffn = dq(b + "post_ffw_norm.weight") if cfg.post_norms else None
+            L.local_rope = bool(cfg.rope_local_theta) and cfg.is_swa(i)
             L.q_norm = dq(b + "attn_q_norm.weight") if cfg.qk_norm else None
             L.k_norm = dq(b + "attn_k_norm.weight") if cfg.qk_norm else None
             L.sinks = dq(b + "attn_sinks.weight") if cfg.attn_sinks else None
@@ -568,7 +616,9 @@ class LlamaCPU:
             self.head = dq("token_embd.weight" if cfg.tie_embeddings else "output.weight")
         inv, self.attn_factor = rope_inv_freq(cfg)
         self.inv_freq = torch.from_numpy(inv)
-        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        inv_l, self.attn_factor_local = rope_inv_freq(cfg, local=True)
+        self.inv_freq_local = torch.from_numpy(inv_l)
+        self.scale = cfg.softmax_scale
 
     linear_state_spec = LlamaGPU.linear_state_spec
 
@@ -589,19 +639,29 @@ class LlamaCPU:
                 L.sg, L.su, L.sd = (dq(b + n) for n in ("ffn_gate_shexp.weight", "ffn_up_shexp.weight",
                                                          "ffn_down_shexp.weight"))
                 L.sgi = dq(b + "ffn_gate_inp_shexp.weight")
+        elif cfg.fused_gate_up:
+            gu = dq(b + "ffn_up.weight")
+            L.wg, L.wu, L.wd = gu[:cfg.ffn], gu[cfg.ffn:], dq(b + "ffn_down.weight")
         else:
             L.wg, L.wu, L.wd = dq(b + "ffn_gate.weight"), dq(b + "ffn_up.weight"), dq(b + "ffn_down.weight")
+
+    def _gate_act(self, g):
+        if self.cfg.act == "gelu":
+            return torch.nn.functional.gelu(g, approximate="tanh")
+        return torch.nn.functional.silu(g)
 
     def _norm(self, x, w):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.rms_eps) * w
 
-    def _rope(self, x, pos):
+    def _rope(self, x, pos, local: bool = False):
         """x [N, heads, d] -> rotated (GGML norm pairs or NEOX halves, partial)."""
         cfg = self.cfg
         rd = cfg.rot_dim
-        ang = pos.to(torch.float32)[:, None] * self.inv_freq[None, :]
-        c = (torch.cos(ang) * self.attn_factor)[:, None, :].to(x.dtype)
-        s = (torch.sin(ang) * self.attn_factor)[:, None, :].to(x.dtype)
+        inv, af = (self.inv_freq_local, self.attn_factor_local) if local else (self.inv_freq,
+                                                                             self.attn_factor)
+        ang = pos.to(torch.float32)[:, None] * inv[None, :]
+        c = (torch.cos(ang) * af)[:, None, :].to(x.dtype)
+        s = (torch.sin(ang) * af)[:, None, :].to(x.dtype)
         out = x.clone()
         if cfg.rope_neox:
             a, b = x[..., : rd // 2], x[..., rd // 2: rd]
@@ -643,10 +703,10 @@ class LlamaCPU:
         if L.moe:
             return self._moe(x, L)
         if b is None:
-            return (torch.nn.functional.silu(x @ L.wg.T) * (x @ L.wu.T)) @ L.wd.T
+            return (self._gate_act(x @ L.wg.T) * (x @ L.wu.T)) @ L.wd.T
         gg = self._lora_cpu(layer, "ffn_gate", x, x @ L.wg.T, b)
         uu = self._lora_cpu(layer, "ffn_up", x, x @ L.wu.T, b)
-        act = torch.nn.functional.silu(gg) * uu
+        act = self._gate_act(gg) * uu
         return self._lora_cpu(layer, "ffn_down", act, act @ L.wd.T, b)
 
     def _deltanet(self, L, x, b, kv):
@@ -724,6 +784,8 @@ class LlamaCPU:
         nq, nkv, d = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         rep = nq // nkv
         h = self.embd[b.tokens.long()].clone() if self.first else h_in.to(self.dtype).clone()
+        if self.first and cfg.embed_scale:
+            h = h * cfg.embed_scale
         if self.first and b.embed_rows is not None:  # image rows spliced into the prompt
             h.index_copy_(0, b.embed_rows.long(), b.embed_vals.to(h.dtype))
         ps = kv.page_size
@@ -750,7 +812,7 @@ class LlamaCPU:
             q, k, v = q.reshape(N, nq, d), k.view(N, nkv, d), v.view(N, nkv, d)
             if L.q_norm is not None:
                 q, k = self._norm(q, L.q_norm), self._norm(k, L.k_norm)
-            q, k = self._rope(q, b.positions), self._rope(k, b.positions)
+            q, k = self._rope(q, b.positions, L.local_rope), self._rope(k, b.positions, L.local_rope)
             K, V = kv.k(li), kv.v(li)
             K[pages, :, offs, :] = k.to(K.dtype)
             V[pages, :, offs, :] = v.to(V.dtype)
@@ -773,6 +835,8 @@ class LlamaCPU:
                 kk = kk.repeat_interleave(rep, dim=1)
                 vv = vv.repeat_interleave(rep, dim=1)
                 s = torch.einsum("hd,nhd->hn", q[t], kk) * self.scale
+                if cfg.attn_softcap:
+                    s = cfg.attn_softcap * torch.tanh(s / cfg.attn_softcap)
                 s = s.masked_fill(~vis[None, :], float("-inf"))
                 if L.sinks is not None:
                     s = torch.cat([s, L.sinks[:, None]], 1)
@@ -786,10 +850,18 @@ class LlamaCPU:
             o = self._lora_cpu(layer, "attn_output", a, a @ L.wo.T, b)
             if L.bo is not None:
                 o = o + L.bo
+            if L.post_attn is not None:
+                o = self._norm(o, L.post_attn)
             h = h + o
             x = self._norm(h, L.ffn_norm)
-            h = h + self._ffn(L, x, layer, b)
+            f = self._ffn(L, x, layer, b)
+            if L.post_ffn is not None:
+                f = self._norm(f, L.post_ffn)
+            h = h + f
         if not self.last:
             return h
         x = self._norm(h[b.sample_rows.long()], self.out_norm)
-        return x @ self.head.T
+        logits = x @ self.head.T
+        if cfg.final_softcap:
+            logits = cfg.final_softcap * torch.tanh(logits / cfg.final_softcap)
+        return logits

@@ -47,15 +47,23 @@ def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
                       (b + "ssm_out.weight", (H, nv * dh), wq)]
         else:
             qrows = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
-            specs += [(b + "attn_q.weight", (qrows, H), wq),
-                      (b + "attn_k.weight", (cfg.kv_dim, H), wq),
-                      (b + "attn_v.weight", (cfg.kv_dim, H), wq),
-                      (b + "attn_output.weight", (H, cfg.q_dim), wq)]
-            if cfg.attn_bias:
-                specs += [(b + "attn_q.bias", (cfg.q_dim,), Q.F32),
-                          (b + "attn_k.bias", (cfg.kv_dim,), Q.F32),
-                          (b + "attn_v.bias", (cfg.kv_dim,), Q.F32),
-                          (b + "attn_output.bias", (H,), Q.F32)]
+            if cfg.fused_qkv:
+                specs.append((b + "attn_qkv.weight", (qrows + 2 * cfg.kv_dim, H), wq))
+                if cfg.attn_bias:
+                    specs.append((b + "attn_qkv.bias", (qrows + 2 * cfg.kv_dim,), Q.F32))
+            else:
+                specs += [(b + "attn_q.weight", (qrows, H), wq),
+                          (b + "attn_k.weight", (cfg.kv_dim, H), wq),
+                          (b + "attn_v.weight", (cfg.kv_dim, H), wq)]
+                if cfg.attn_bias:
+                    specs += [(b + "attn_q.bias", (cfg.q_dim,), Q.F32),
+                              (b + "attn_k.bias", (cfg.kv_dim,), Q.F32),
+                              (b + "attn_v.bias", (cfg.kv_dim,), Q.F32)]
+            specs.append((b + "attn_output.weight", (H, cfg.q_dim), wq))
+            if cfg.has_out_bias:
+                specs.append((b + "attn_output.bias", (H,), Q.F32))
+            if cfg.post_norms:
+                specs.append((b + "post_attention_norm.weight", (H,), Q.F32))
             if cfg.qk_norm:
                 specs += [(b + "attn_q_norm.weight", (cfg.head_dim,), Q.F32),
                           (b + "attn_k_norm.weight", (cfg.head_dim,), Q.F32)]
@@ -79,10 +87,15 @@ def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
                           (b + "ffn_up_shexp.weight", (S, H), wq),
                           (b + "ffn_down_shexp.weight", (H, S), wq),
                           (b + "ffn_gate_inp_shexp.weight", (H,), Q.F32)]
+        elif cfg.fused_gate_up:
+            specs += [(b + "ffn_up.weight", (2 * cfg.ffn, H), wq),
+                      (b + "ffn_down.weight", (H, cfg.ffn), wq)]
         else:
             specs += [(b + "ffn_gate.weight", (cfg.ffn, H), wq),
                       (b + "ffn_up.weight", (cfg.ffn, H), wq),
                       (b + "ffn_down.weight", (H, cfg.ffn), wq)]
+        if cfg.post_norms and not cfg.is_linear_attn(i):
+            specs.append((b + "post_ffw_norm.weight", (H,), Q.F32))
     specs.append(("output_norm.weight", (H,), Q.F32))
     if not cfg.tie_embeddings:
         specs.append(("output.weight", (cfg.vocab, H), oq))
@@ -90,7 +103,7 @@ def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
 
 
 def _is_norm(name: str) -> bool:
-    return name.endswith("norm.weight")
+    return name.endswith("norm.weight") or name.endswith("norm.weight.post")
 
 
 def _init_value(name: str, shape, rng: np.random.Generator, std: float) -> np.ndarray:
@@ -116,6 +129,12 @@ class GgufSource:
         else:
             self.f = GGUFReader(path)
         self.cfg = from_gguf_metadata(self.f.metadata)
+        # LongRoPE (phi3): per-pair frequency divisors stored as tensors; the
+        # short factors serve contexts up to the original training length
+        for name in ("rope_factors_short.weight", "rope_factors_long.weight"):
+            if self.cfg.rope_factors is None and name in self.f.tensors:
+                t, qt, shape = self.get(name)
+                self.cfg.rope_factors = Q.dequantize(t.numpy().reshape(-1), qt).tolist()
 
     def has(self, name: str) -> bool:
         return name in self.f.tensors
@@ -201,7 +220,7 @@ def _random_blocks_device(name, shape, qt, seed, std, device) -> torch.Tensor:
 def write_random_gguf(cfg: ModelConfig, path: str, seed: int = 0, std: float = 0.02):
     """Write a complete random-init GGUF (host generation; for test-size models)."""
     src = RandomSource(cfg, seed=seed, std=std)
-    w = GGUFWriter({"llama": "llama", "gpt-oss": "gpt-oss", "qwen3next": "qwen3next"}[cfg.arch])
+    w = GGUFWriter(cfg.arch)
     for k, v in to_gguf_metadata(cfg).items():
         w.add(k, v)
     for name, shape, qt in tensor_specs(cfg):
