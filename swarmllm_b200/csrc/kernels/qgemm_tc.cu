@@ -60,10 +60,15 @@ struct QCfg {
   static constexpr int U = DQ;                           // unit stages in flight
   static constexpr int THREADS = 96 + 128 * DQ;          // W producer, MMA, X producer, DQ WGs
   static constexpr int FIRST_DQ_WARP = 3;
-  static constexpr int A_COL = kTmemCols - 128 * U;      // D uses columns [0, N)
+  static constexpr int A_COL = kTmemCols - 128 * U;      // accumulators use [0, NACC * N)
+  // Independent accumulators the 16 MMAs of a unit rotate over.  At decode
+  // sizes a 128 x N x 16 MMA is short, and MMAs that accumulate into the same
+  // TMEM columns wait for each other; rotating over NACC accumulators keeps
+  // NACC of them in flight.  The drain adds the accumulators.
+  static constexpr int NACC = (A_COL / N) >= 4 ? 4 : ((A_COL / N) >= 2 ? 2 : 1);
   static constexpr int X_UNIT_BYTES = N * 512;           // N rows x 256 K fp16 (4 swizzle atoms)
   static constexpr int W_ST = 2 * DQ;
-  static_assert(A_COL >= N, "TMEM budget");
+  static_assert(A_COL >= NACC * N, "TMEM budget");
   static constexpr int X_BYTES = U * X_UNIT_BYTES;
   static constexpr int W_BYTES = W_ST * kWStageBytes;
   static constexpr int BAR_BYTES = 512;
@@ -214,11 +219,13 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
         tc_fence_after();
         const uint64_t xd = xdesc[0] + (uint64_t)((s * C::X_UNIT_BYTES) >> 4);
         const uint32_t ab = tmem_base + C::A_COL + s * 128;
-        umma_f16_ts(tmem_base, ab, xd, idesc, first ? 0u : 1u);
 #pragma unroll
-        for (int kk = 1; kk < 16; ++kk)
-          umma_f16_ts(tmem_base, ab + kk * 8, xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4),
-                      idesc, 1u);
+        for (int kk = 0; kk < 16; ++kk) {
+          const uint32_t acc = (uint32_t)((kk % C::NACC) * N);
+          umma_f16_ts(tmem_base + acc, ab + kk * 8,
+                      xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4), idesc,
+                      (first && kk < C::NACC) ? 0u : 1u);
+        }
         umma_commit(&empty[s]);
         if (last) {
           umma_commit(d_full);
@@ -282,6 +289,15 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
             uint32_t r[16];
             tmem_ld_x16(tmem_base + lane_off + c * 16, r);
             tmem_wait_ld();
+#pragma unroll
+            for (int acc = 1; acc < C::NACC; ++acc) {
+              uint32_t r2[16];
+              tmem_ld_x16(tmem_base + lane_off + acc * N + c * 16, r2);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                r[e] = __float_as_uint(__uint_as_float(r[e]) + __uint_as_float(r2[e]));
+            }
             if (a.n_peers == 0) {
               float* dst = a.ws + off;
 #pragma unroll

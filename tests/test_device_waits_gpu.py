@@ -36,9 +36,10 @@ def test_flag_wait_times_out_and_stream_continues():
     # the stream and the context are still usable
     y = torch.arange(10, device=DEV, dtype=torch.float32).sum()
     assert float(y) == 45.0
-    # the same wait passes once the flags reach the next epoch
+    # a wait that gave up still consumed its epoch (every rank counts waits in
+    # lockstep): the next wait passes once the flags reach epoch 2
     status.zero_()
-    flags.fill_(1)
+    flags.fill_(2)
     C().flag_wait(flags.data_ptr(), 4, ctl, 2, status, 77, TIMEOUT_NS)
     torch.cuda.synchronize()
     assert status.cpu().tolist()[0] == 0
