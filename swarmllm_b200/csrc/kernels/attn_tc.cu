@@ -98,6 +98,7 @@ template <int D, bool TREE, int REP>
 __global__ void __launch_bounds__(192, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                    const __grid_constant__ CUtensorMap v_map, AttnTcArgs a) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   using C = AttnCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &

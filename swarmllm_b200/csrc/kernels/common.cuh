@@ -17,6 +17,37 @@ namespace swarm {
 
 constexpr int kWarp = 32;
 
+// Programmatic dependent launch (PDL).  The weight-streaming GEMM / GEMV
+// kernels are launched with programmatic stream serialisation: they may start
+// while the kernel before them is still running, stream their first weight
+// tiles, and call pdl_wait() before reading activations or writing results
+// (it returns once the previous grid has completed and its writes are
+// visible).  The kernels that usually precede them call pdl_trigger() first
+// thing, which lets the dependent grid launch as soon as every CTA of the
+// current grid is running.  Both are no-ops for launches without the attribute.
+SW_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+SW_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host: whether launches opt into PDL (SWARMLLM_PDL=0 turns it off).
+bool pdl_enabled();
+
+// Launch `kernel` with programmatic stream serialisation (when enabled).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // cudaFuncSetAttribute applies to the device current at the call, so a launcher
 // that raises a kernel's dynamic shared-memory limit must do it once on every
 // device it launches on.  `done` is the launcher's bit mask of devices already

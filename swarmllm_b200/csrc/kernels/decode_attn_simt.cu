@@ -39,6 +39,7 @@ struct DecodeAttnArgs {
 
 template <int D, int NREP>
 __global__ void __launch_bounds__(128) decode_attn_split_kernel(DecodeAttnArgs a) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   const int t = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = a.seq_lens[t];
@@ -149,6 +150,7 @@ __global__ void decode_attn_combine_kernel(const float* __restrict__ part_o,
                                            const float* __restrict__ part_ml, int n_splits, int D,
                                            const float* __restrict__ sinks, int n_q,
                                            __half* __restrict__ out) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   const int row = blockIdx.x;  // t * n_q + h
   const int h = row % n_q;
   const float* ml = part_ml + (size_t)row * n_splits * 2;

@@ -47,6 +47,7 @@ __global__ void ssm_conv_silu_kernel(GemmOut g, const float* __restrict__ w, int
                                      const float* __restrict__ state,
                                      const int4* __restrict__ seqs, int S,
                                      float* __restrict__ out) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   const int r = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
@@ -103,6 +104,7 @@ __global__ void __launch_bounds__(D) delta_rule_kernel(
     const float* __restrict__ dt_bias, const float* __restrict__ A, GemmOut gz,
     const float* __restrict__ norm_w, float eps, float* __restrict__ state,
     const int4* __restrict__ seqs, __half* __restrict__ out) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   static_assert(D == 128, "one thread per value channel, 4 warps");
   __shared__ float qs[D], ks[D], red[8];
   const int s = blockIdx.x, h = blockIdx.y, j = threadIdx.x;

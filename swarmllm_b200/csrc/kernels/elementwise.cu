@@ -27,6 +27,7 @@ namespace swarm {
 
 __global__ void embed_gather_kernel(const uint8_t* __restrict__ table, int type, int hidden,
                                     const int32_t* __restrict__ ids, float* __restrict__ out) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   const int t = blockIdx.x;
   const int id = ids[t];
   const int bv = ggml_block_values(type), bb = ggml_block_bytes(type);
@@ -41,6 +42,7 @@ __global__ void embed_gather_kernel(const uint8_t* __restrict__ table, int type,
 template <int kThreads>
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                __half* __restrict__ out, int dim, float eps) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   __shared__ float red[32];
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * dim;
@@ -60,6 +62,7 @@ __global__ void epi_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ resid
                                             const float* __restrict__ w,
                                             __half* __restrict__ out, float eps,
                                             int out_stride) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   extern __shared__ float row[];
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -146,6 +149,7 @@ __global__ void epi_postnorm_residual_rmsnorm_kernel(GemmOut g, float* __restric
                                                      const float* __restrict__ w,
                                                      __half* __restrict__ out, float eps,
                                                      int out_stride) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   extern __shared__ float row[];
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -351,6 +355,7 @@ SW_DEVICE float gelu_tanh(float x) {
 __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int F, int kind,
                                   int interleaved, float alpha, float limit,
                                   __half* __restrict__ out) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   const int t = blockIdx.y;
   if (!interleaved && (F & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
     // eight features per thread and step: one partial-sum lookup per eight, 16-byte stores
@@ -444,6 +449,7 @@ __global__ void epi_copy_kernel(GemmOut g, const float* __restrict__ bias, float
 }
 
 __global__ void mul_f16_kernel(__half* __restrict__ x, const __half* __restrict__ y, size_t n) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     x[i] = __hmul(x[i], y[i]);
@@ -483,6 +489,7 @@ constexpr int kClusterNorm = 8;
 __global__ void __launch_bounds__(256) epi_residual_rmsnorm_cluster_kernel(
     GemmOut g, float* __restrict__ residual, const float* __restrict__ bias,
     const float* __restrict__ w, __half* __restrict__ out, float eps, int out_stride) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float part;
   __shared__ float red[32];

@@ -494,6 +494,7 @@ __global__ void __launch_bounds__(512) moe_combine_kernel(
     const float* __restrict__ rows, int row_stride, const float* __restrict__ wts, int k,
     GemmOut sh, int has_sh, GemmOut shg, int has_shg, float* __restrict__ residual, int H,
     const float* __restrict__ norm_w, __half* __restrict__ out, int out_stride, float eps) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   extern __shared__ float crow[];
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -710,6 +711,7 @@ __global__ void __launch_bounds__(256) moe_combine_cluster_kernel(
     const float* __restrict__ rows, int row_stride, const float* __restrict__ wts, int k,
     GemmOut sh, int has_sh, GemmOut shg, int has_shg, float* __restrict__ residual, int H,
     const float* __restrict__ norm_w, __half* __restrict__ out, int out_stride, float eps) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float part;
   __shared__ float red[32];

@@ -176,6 +176,7 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
   } else if (warp == 2) {
     // ------------------------------------------------------------ X producer
     if (lane == 0) {
+      pdl_wait();  // activations come from the previous kernel; weights did not wait
       int issued = 0;
       bool ok = true;
       int tile = (int)(u0 / a.ksb), sb = (int)(u0 - (long)tile * a.ksb);
@@ -424,6 +425,9 @@ static int q_env(const char* name, int dflt) {
   const char* v = getenv(name);
   return v ? atoi(v) : dflt;
 }
+
+static const bool g_pdl = q_env("SWARMLLM_PDL", 1) != 0;
+bool swarm::pdl_enabled() { return g_pdl; }
 static const int g_gemv_max_t = [] {
   const int v = q_env("SWARMLLM_QGEMV_MAX_T", kQGemvMaxT);
   return v < 0 ? 0 : (v > kQGemvMaxT ? kQGemvMaxT : v);
@@ -461,7 +465,9 @@ static int launch_n(const CUtensorMap& map, const QGemmArgs& a, int n_ctas, cuda
   using C = QCfg<N>;
   static unsigned long long attr_done = 0;
   if (!smem_attr_once(qgemm_q4k_tc_kernel<N>, C::SMEM, &attr_done)) return -3;
-  qgemm_q4k_tc_kernel<N><<<n_ctas, C::THREADS, C::SMEM, s>>>(map, a);
+  if (launch_pdl(qgemm_q4k_tc_kernel<N>, dim3(n_ctas), dim3(C::THREADS), C::SMEM, s, map, a) !=
+      cudaSuccess)
+    return -4;
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

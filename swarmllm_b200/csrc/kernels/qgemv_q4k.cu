@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(kGvWarps * 32)
     if (++x_sb == a.ksb) x_sb = 0;
   };
   if (lane == 0) {
-    while (w_next < min(n, kGvWStages)) issue_w();
+    while (w_next < min(n, kGvWStages)) issue_w();   // weights: independent of the previous kernel
+    pdl_wait();                                      // activations and results: after it
     while (x_next < min(n, kGvXStages)) issue_x();
   }
 
@@ -278,7 +279,9 @@ static int occupancy_t() {
 template <int T>
 static int launch_t(const GemvArgs& a, int ctas, cudaStream_t s) {
   if (setup_t<T>() != 1) return -3;
-  qgemv_q4k_kernel<T><<<ctas, kGvWarps * 32, GvCfg<T>::SMEM, s>>>(a);
+  if (launch_pdl(qgemv_q4k_kernel<T>, dim3(ctas), dim3(kGvWarps * 32), GvCfg<T>::SMEM, s, a) !=
+      cudaSuccess)
+    return -4;
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

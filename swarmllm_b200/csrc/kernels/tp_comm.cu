@@ -97,6 +97,7 @@ SW_DEVICE float4 add4(float4 a, float4 b) {
 // Work unit u = t * C + j: slice j of row t.  Phase 2 (reduce + publish) covers
 // the rank's own columns of the slice, phase 3 (normalise) 1/C of the whole row.
 __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const TpReduceArgs a) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
   __shared__ float red[32];
   __shared__ int ok_s;
   const int H = a.H, W = a.W, C = a.C;
