@@ -388,7 +388,10 @@ class LlamaGPU:
         ao = ctx.attn_out[:N]
         act = ctx.act[:N]
         P = self._stage_ctx()
+        lev = getattr(self, "layer_events", None)   # per-layer CUDA events (layout planner)
         for j, L in enumerate(self.layers):
+            if lev is not None:
+                lev[j].record()
             if L.linear:
                 with P("delta_rule"):
                     self._deltanet(L, b, kv, ctx, x, N)
@@ -446,6 +449,8 @@ class LlamaGPU:
             with P("ffn_down+norm"):
                 g = self._lora(j, "down", act, self._row_parallel(L.wdown, act, ctx), ctx, b)
                 self._residual_norm(g, h, None, nxt_w, nxt_out, ctx, L.post_ffn_norm)
+        if lev is not None:
+            lev[len(self.layers)].record()
         if not self.last:
             return h
         with P("lm_head"):

@@ -59,7 +59,9 @@ class AsyncPipelineEngine:
         self.stage, self.S = self.rank // tp, self.world // tp
         self.device = torch.device(device)
         self.gpu = self.device.type == "cuda"
-        self.bounds = stage_bounds(cfg.n_layers, self.S, 0.5, 1.0)
+        from .planner import layer_costs
+        self.bounds = stage_bounds(cfg.n_layers, self.S,
+                                   costs=layer_costs(cfg, max(1, ecfg.max_running), 2048, tp))
         lo, hi = self.bounds[self.stage], self.bounds[self.stage + 1]
         self.lo, self.hi = lo, hi
         self.root = self.rank == 0

@@ -19,8 +19,10 @@ src/network/protocol/layer_forward.rs:6), one request at a time.  Here:
 * activations cross as the fp32 residual stream, so a split run is
   bit-identical to a single-process run of the same batch (the two-CPU-peer tiny Llama setup).
 
-Stage boundaries come from the native planner (`plan_bottleneck`, uniform
-per-layer cost on one NVSwitch box).
+Stage boundaries come from the native planner (`plan_bottleneck`) over
+per-layer costs from the layout planner (parallel/planner.py): what each layer
+reads per decode step, so attention / linear-attention / MoE layers weigh
+what they cost.
 """
 from __future__ import annotations
 
@@ -42,9 +44,15 @@ from ..ops.attention import PagedKVCache
 from ..utils.ext import native
 
 
-def stage_bounds(n_layers: int, n_stages: int, extra_first: float = 0.0, extra_last: float = 0.0):
-    """Layer boundaries [S+1] minimising the slowest stage (embedding and LM
-    head cost folded into the first / last layer)."""
+def stage_bounds(n_layers: int, n_stages: int, extra_first: float = 0.0, extra_last: float = 0.0,
+                 costs: list | None = None):
+    """Layer boundaries [S+1] minimising the slowest stage.  `costs`: per-layer
+    cost (parallel/planner.py layer_costs: what each layer reads per decode
+    step, or measured timings); without it every layer costs 1 with the
+    embedding and LM head folded into the first / last layer."""
+    if costs is not None:
+        from .planner import stage_plan
+        return stage_plan(costs, [0.0] * n_layers, n_stages)[0]
     cost = [1.0] * n_layers
     cost[0] += extra_first
     cost[-1] += extra_last
@@ -82,7 +90,9 @@ class PipelineEngine:
         self.stage, self.n_stages = self.rank // tp, self.world // tp
         self.device = torch.device(device)
         self.gpu = self.device.type == "cuda"
-        self.bounds = stage_bounds(cfg.n_layers, self.n_stages, 0.5, 1.0)
+        from .planner import layer_costs
+        self.bounds = stage_bounds(cfg.n_layers, self.n_stages,
+                                   costs=layer_costs(cfg, max(1, ecfg.max_running), 2048, tp))
         lo, hi = self.bounds[self.stage], self.bounds[self.stage + 1]
         self.lo, self.hi = lo, hi
         self.root = self.rank == 0  # owns the scheduler and the KV block manager
