@@ -1,8 +1,8 @@
 """Standalone cases of the hot kernels, for profiling one kernel at a time:
 
     python -m swarmllm_b200.utils.kernel_cases \
-        {qgemm|qgemv|qgemv_o|dense|attn|attn_prefill|rmsnorm|swiglu|rope_kv|moe|delta|delta_decode|
-         tree_rank|sample} [--time]
+        {qgemm|qgemm_sweep|qgemv|qgemv_o|dense|attn|attn_prefill|rmsnorm|swiglu|rope_kv|moe|delta|
+         delta_decode|tree_rank|sample} [--time]
 
 Each case builds benchmark-sized operands on cuda:0 (inputs larger than the
 126 MB L2 where memory traffic matters; tree_rank and sample use the real
@@ -46,7 +46,28 @@ def run_case(which: str, TIME: bool = False) -> None:
     """Build one case's operands on cuda:0 and run its kernel a few times."""
     torch.manual_seed(0)
     _CASE[0] = which
-    if which == "qgemm":       # Llama-3.3-70B gate|up at decode batch 32 (264 MB of weights)
+    if which == "qgemm_sweep":  # the 70B projections at 1..2048 tokens: device time, GB/s, TFLOP/s
+        from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+        for rows, K, name in ((57344, 8192, "gate_up"), (8192, 28672, "down"), (8192, 8192, "o_proj")):
+            lin = QLinear(rand_q4k(rows, K), Q.Q4_K, rows, K, dev)
+            for T in (1, 3, 8, 16, 32, 64, 128, 2048):
+                ws = GemmWorkspace(dev, T, rows)
+                x = torch.randn(T, K, device=dev).half()
+                for _ in range(3):
+                    lin(x, ws)
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                n = 20 if T < 1024 else 5
+                a.record()
+                for _ in range(n):
+                    lin(x, ws)
+                b.record()
+                torch.cuda.synchronize()
+                us = a.elapsed_time(b) * 1000 / n
+                print(f"{name} {rows}x{K} T={T}: {us:8.1f} us  {rows * K * 0.5625 / us / 1e3:6.0f} GB/s"
+                      f"  {2 * rows * K * T / us / 1e6:7.1f} TFLOP/s", flush=True)
+                ws.check()
+    elif which == "qgemm":       # Llama-3.3-70B gate|up at decode batch 32 (264 MB of weights)
         from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
         rows, K, T = 57344, 8192, 32
         lin = QLinear(rand_q4k(rows, K), Q.Q4_K, rows, K, dev)
