@@ -90,6 +90,46 @@ void moe_combine(Tensor rows, Tensor wts, int64_t k, const GemmResult* sh, const
   TORCH_CHECK(rc == 0, "moe_combine failed: rc=", rc);
 }
 
+void moe_localize(Tensor ids, Tensor wts, Tensor counts, int64_t E, int64_t e0, int64_t n_loc) {
+  CHECK_DT(ids, at::kInt); CHECK_DT(wts, at::kFloat); CHECK_DT(counts, at::kInt);
+  const at::cuda::CUDAGuard guard(ids.device());
+  TORCH_CHECK(launch_moe_localize(ids.data_ptr<int32_t>(), wts.data_ptr<float>(),
+                                  counts.data_ptr<int>(), (int)ids.numel(), (int)E, (int)e0,
+                                  (int)n_loc, cur_stream()) == 0, "moe_localize failed");
+}
+
+// This rank's MoE partial into the owners' receive slots; returns the dense
+// GemmOut over all W slots of this rank's receive buffer (for tp_reduce_norm).
+GemmResult moe_combine_tp(Tensor rows, Tensor wts, int64_t k, const GemmResult* sh,
+                          const GemmResult* shg, int64_t T, int64_t H, int64_t recv_base,
+                          int64_t src_stride, std::vector<int64_t> dst_ptrs, Tensor sig_ctl,
+                          std::vector<int64_t> sig_bases, int64_t sig_flag_off, int64_t rank) {
+  CHECK_DT(rows, at::kFloat); CHECK_DT(wts, at::kFloat); CHECK_DT(sig_ctl, at::kInt);
+  TORCH_CHECK(!dst_ptrs.empty() && dst_ptrs.size() <= 8 && dst_ptrs.size() == sig_bases.size(),
+              "1..8 ranks");
+  const at::cuda::CUDAGuard guard(rows.device());
+  unsigned long long d[8], b[8];
+  for (size_t i = 0; i < dst_ptrs.size(); ++i) {
+    d[i] = (unsigned long long)dst_ptrs[i];
+    b[i] = (unsigned long long)sig_bases[i];
+  }
+  const int W = (int)dst_ptrs.size();
+  int rc = launch_moe_combine_tp(rows.data_ptr<float>(), (int)rows.stride(0), wts.data_ptr<float>(),
+                                 (int)k, sh ? &sh->g : nullptr, shg ? &shg->g : nullptr, (int)T,
+                                 (int)H, W, d, sig_ctl.data_ptr<int>(), b,
+                                 (long long)sig_flag_off, (int)rank, cur_stream());
+  TORCH_CHECK(rc == 0, "moe_combine_tp failed: rc=", rc);
+  GemmResult r;
+  r.g = swarm::GemmOut{};
+  r.g.ws = reinterpret_cast<const float*>(recv_base);
+  r.g.rows = (int)H;
+  r.g.T = (int)T;
+  r.g.mode = 0;
+  r.g.n_src = W;
+  r.g.src_stride = src_stride;
+  return r;
+}
+
 void mxfp4_repack(Tensor src, int64_t rows, int64_t K, Tensor dst) {
   CHECK_CUDA(src); CHECK_CUDA(dst);
   TORCH_CHECK(dst.numel() * dst.element_size() >= moe_packed_bytes(1, (int)rows, (int)K),
@@ -115,6 +155,11 @@ void register_moe_ops(py::module& m) {
   m.def("moe_combine", &moe_combine, py::arg("rows"), py::arg("wts"), py::arg("k"),
         py::arg("sh").none(true), py::arg("shg").none(true), py::arg("residual"),
         py::arg("norm_w"), py::arg("out"), py::arg("eps"));
+  m.def("moe_localize", &moe_localize);
+  m.def("moe_combine_tp", &moe_combine_tp, py::arg("rows"), py::arg("wts"), py::arg("k"),
+        py::arg("sh").none(true), py::arg("shg").none(true), py::arg("T"), py::arg("H"),
+        py::arg("recv_base"), py::arg("src_stride"), py::arg("dst_ptrs"), py::arg("sig_ctl"),
+        py::arg("sig_bases"), py::arg("sig_flag_off"), py::arg("rank"));
   m.def("mxfp4_repack", &mxfp4_repack);
   m.def("moe_packed_bytes", &moe_packed_bytes);
   m.def("moe_tok_tile", &moe_tok_tile);

@@ -10,11 +10,12 @@
 // copy) sums the segments while it reads, which saves one write + read of the
 // [T, rows] result.
 //
-// mode 0 is a plain dense [T][rows] fp32 buffer (SIMT GEMM, tests).
-// n_src > 1: the partials of n_src ranks of a tensor-parallel group, pushed
-// into this rank's buffer by their GEMM epilogues, sit src_stride floats
-// apart; get() then also sums over the ranks (the all-reduce happens while
-// reading).
+// mode 0 is a plain dense [T][rows] fp32 buffer (SIMT GEMM, tests, the MoE
+// combine's per-rank partials under tensor parallelism).
+// n_src > 1 (either mode): the partials of n_src ranks of a tensor-parallel
+// group, stored into this rank's buffer by their epilogues, sit src_stride
+// floats apart; get() then also sums over the ranks (the reduction happens
+// while reading).
 // The struct is plain data so host C++ (the torch bindings) can hold it.
 #pragma once
 #include <stddef.h>
@@ -51,7 +52,12 @@ struct GemmOut {
 
   __device__ __forceinline__ float get(int t, int r) const {
     const float extra = add ? add[(size_t)t * add_stride + r] : 0.f;
-    if (mode == 0) return ws[(size_t)t * rows + r] + extra;
+    if (mode == 0) {
+      float acc = extra;
+      const int ns = n_src > 1 ? n_src : 1;
+      for (int s = 0; s < ns; ++s) acc += ws[(size_t)s * src_stride + (size_t)t * rows + r];
+      return acc;
+    }
     const int rt = r >> 7, rr = r & 127;
     const int nt = t >> tok_shift, tt = t & (tok_tile - 1);
     const int tile = rt * n_tok_tiles + nt;
@@ -77,8 +83,13 @@ struct GemmOut {
       acc = make_float4(a[0], a[1], a[2], a[3]);
     }
     if (mode == 0) {
-      const float4 v = *reinterpret_cast<const float4*>(ws + (size_t)t * rows + r);
-      return make_float4(acc.x + v.x, acc.y + v.y, acc.z + v.z, acc.w + v.w);
+      const int ns = n_src > 1 ? n_src : 1;
+      for (int s = 0; s < ns; ++s) {
+        const float4 v =
+            *reinterpret_cast<const float4*>(ws + (size_t)s * src_stride + (size_t)t * rows + r);
+        acc = make_float4(acc.x + v.x, acc.y + v.y, acc.z + v.z, acc.w + v.w);
+      }
+      return acc;
     }
     const int rt = r >> 7, rr = r & 127;
     const int nt = t >> tok_shift, tt = t & (tok_tile - 1);
@@ -113,11 +124,14 @@ struct GemmOut {
     }
     const float* base;
     if (mode == 0) {
-      base = ws + (size_t)t * rows + r;
-      const float4 v0 = *reinterpret_cast<const float4*>(base);
-      const float4 v1 = *reinterpret_cast<const float4*>(base + 4);
-      lo = make_float4(lo.x + v0.x, lo.y + v0.y, lo.z + v0.z, lo.w + v0.w);
-      hi = make_float4(hi.x + v1.x, hi.y + v1.y, hi.z + v1.z, hi.w + v1.w);
+      const int ns = n_src > 1 ? n_src : 1;
+      for (int s = 0; s < ns; ++s) {
+        base = ws + (size_t)s * src_stride + (size_t)t * rows + r;
+        const float4 v0 = *reinterpret_cast<const float4*>(base);
+        const float4 v1 = *reinterpret_cast<const float4*>(base + 4);
+        lo = make_float4(lo.x + v0.x, lo.y + v0.y, lo.z + v0.z, lo.w + v0.w);
+        hi = make_float4(hi.x + v1.x, hi.y + v1.y, hi.z + v1.z, hi.w + v1.w);
+      }
       return;
     }
     const int rt = r >> 7, rr = r & 127;

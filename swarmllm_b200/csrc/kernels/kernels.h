@@ -126,6 +126,14 @@ int launch_moe_combine(const float* rows, int row_stride, const float* wts, int 
                        int T, int H, const float* norm_w, __half* out, int out_stride, float eps,
                        cudaStream_t s);
 
+// Tensor parallelism over the experts (every rank: every token, experts [e0, e0+n_loc)).
+int launch_moe_localize(int32_t* ids, float* wts, int* counts, int P, int E, int e0, int n_loc,
+                        cudaStream_t s);
+int launch_moe_combine_tp(const float* rows, int row_stride, const float* wts, int k,
+                          const swarm::GemmOut* sh, const swarm::GemmOut* shg, int T, int H, int W,
+                          const unsigned long long* dst, int* ctl, const unsigned long long* bases,
+                          long long flag_off, int rank, cudaStream_t s);
+
 void launch_mul_f16(__half* x, const __half* y, size_t n, cudaStream_t s);
 
 // ---- gated DeltaNet (deltanet.cu) --------------------------------------------

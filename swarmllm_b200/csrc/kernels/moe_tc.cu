@@ -168,7 +168,7 @@ __global__ void moe_scatter_kernel(const __half* __restrict__ x, int x_stride, i
                                    int32_t* __restrict__ ret, int rank_bits) {
   const int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (p >= P) return;
+  if (p >= P || ids[p] < 0) return;  // -1: routed to another rank's expert (TP)
   int pos = 0;
   if (lane == 0) {
     pos = atomicAdd(&cursor[ids[p]], 1);
@@ -517,6 +517,56 @@ __global__ void __launch_bounds__(512) moe_combine_kernel(
     out[(size_t)t * out_stride + i] = __float2half_rn(crow[i] * inv * norm_w[i]);
 }
 
+// ============================================================== tensor parallelism
+// Under tensor parallelism every rank of the group holds every token and
+// experts [e0, e0 + n_loc).  moe_localize keeps this rank's (token, k) pairs:
+// their expert ids become local, the others get id -1 and weight 0; the
+// per-expert counts move to [0, n_loc) and the rest are cleared (moe_plan
+// expects zero counts on entry of the next layer).  One CTA.
+__global__ void moe_localize_kernel(int32_t* __restrict__ ids, float* __restrict__ wts,
+                                    int* __restrict__ counts, int P, int E, int e0, int n_loc) {
+  __shared__ int sc[1024];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) sc[e] = counts[e];
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) counts[e] = e < n_loc ? sc[e0 + e] : 0;
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    const int e = ids[p];
+    if (e >= e0 && e < e0 + n_loc) {
+      ids[p] = e - e0;
+    } else {
+      ids[p] = -1;
+      wts[p] = 0.f;
+    }
+  }
+}
+
+// This rank's share of the MoE output, v = sum_j w[t,j] * rows[t*k+j] (its own
+// experts; w = 0 for the others) + gate * shared (its slice of the shared
+// expert's down projection), stored column block by column block into the
+// receive slot of the rank that owns those columns (dst[o] + t * H + c, over
+// NVLink for the other ranks); the CTA that finishes last raises this rank's
+// done flag on every rank.  tp_reduce_norm then sums the W slots, adds the
+// residual and normalises (tp_comm.cu).  One CTA per token.
+__global__ void __launch_bounds__(256) moe_combine_tp_kernel(
+    const float* __restrict__ rows, int row_stride, const float* __restrict__ wts, int k,
+    GemmOut sh, int has_sh, GemmOut shg, int has_shg, int H, int W, EpPeers dst, int* ctl,
+    EpPeers sig, long long flag_off, int rank) {
+  const int t = blockIdx.x;
+  const int per = H / W;
+  float gate = 1.f;
+  if (has_shg) gate = 1.f / (1.f + __expf(-shg.get(t, 0)));
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float v = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const float w = wts[t * k + j];
+      if (w != 0.f) v += w * rows[(size_t)(t * k + j) * row_stride + i];
+    }
+    if (has_sh) v += gate * sh.get(t, i);
+    reinterpret_cast<float*>(dst.base[i / per])[(size_t)t * H + i] = v;
+  }
+  ep_grid_done_signal(ctl, sig.base, flag_off, W, rank);
+}
+
 // ============================================================== repack
 // GGUF MXFP4 [rows][K/32 blocks of 17 B] (one expert) -> [row_tiles][units]
 // [128 rows][8 + 16 nb] with the nibble order of dq_mx_word.  Padding rows
@@ -776,5 +826,30 @@ int launch_moe_combine(const float* rows, int row_stride, const float* wts, int 
   moe_combine_kernel<<<T, 512, smem, s>>>(rows, row_stride, wts, k, sh ? *sh : z, sh != nullptr,
                                           shg ? *shg : z, shg != nullptr, residual, H, norm_w,
                                           out, out_stride ? out_stride : H, eps);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
+int launch_moe_localize(int32_t* ids, float* wts, int* counts, int P, int E, int e0, int n_loc,
+                        cudaStream_t s) {
+  if (E > 1024 || e0 < 0 || n_loc <= 0 || e0 + n_loc > E) return -1;
+  moe_localize_kernel<<<1, 1024, 0, s>>>(ids, wts, counts, P, E, e0, n_loc);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
+}
+
+int launch_moe_combine_tp(const float* rows, int row_stride, const float* wts, int k,
+                          const GemmOut* sh, const GemmOut* shg, int T, int H, int W,
+                          const unsigned long long* dst, int* ctl, const unsigned long long* bases,
+                          long long flag_off, int rank, cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (W < 1 || W > 8 || H % W) return -1;
+  GemmOut z{};
+  EpPeers d{}, b{};
+  for (int i = 0; i < W; ++i) {
+    d.base[i] = dst[i];
+    b.base[i] = bases[i];
+  }
+  moe_combine_tp_kernel<<<T, 256, 0, s>>>(rows, row_stride, wts, k, sh ? *sh : z,
+                                          (int)(sh != nullptr), shg ? *shg : z,
+                                          (int)(shg != nullptr), H, W, d, ctl, b, flag_off, rank);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }

@@ -29,7 +29,8 @@ from ..gguf import quants as Q
 from ..ops.attention import AttentionWorkspace, PagedKVCache, paged_attention
 from ..ops.linear import GemmWorkspace, QLinear
 from ..parallel.tp import split_cols, split_rows
-from ..ops.moe import MoeExperts, MoeWorkspace, moe_experts, moe_experts_ep, moe_route
+from ..ops.moe import (MoeExperts, MoeWorkspace, moe_experts, moe_experts_ep, moe_experts_tp,
+                       moe_route)
 from ..utils.ext import C
 from .config import ModelConfig, rope_inv_freq
 
@@ -79,11 +80,21 @@ class LlamaGPU:
         self.lora = None
         W = tp.world if tp else 1
         tr = tp.rank if tp else 0
-        assert cfg.n_heads % W == 0 and cfg.n_kv_heads % W == 0 and cfg.ffn % W == 0
-        self.n_q, self.n_kv, self.ffn_loc = cfg.n_heads // W, cfg.n_kv_heads // W, cfg.ffn // W
-        if tp is not None:
-            assert not cfg.n_experts and not cfg.full_attn_interval, \
-                "tensor parallelism covers the dense attention + SwiGLU families"
+        assert cfg.n_heads % W == 0 and cfg.ffn % W == 0
+        self.n_q, self.ffn_loc = cfg.n_heads // W, cfg.ffn // W
+        # KV heads of this rank's query heads: an even split, or -- with fewer KV
+        # heads than ranks -- the one KV head its query heads share, replicated
+        rep = cfg.n_heads // cfg.n_kv_heads
+        self.kv0 = (tr * self.n_q) // rep
+        self.n_kv = ((tr + 1) * self.n_q - 1) // rep + 1 - self.kv0
+        assert cfg.n_kv_heads % W == 0 or (W % cfg.n_kv_heads == 0 and self.n_q <= rep), \
+            "query heads of a rank must map onto whole KV heads"
+        # linear-attention heads (gated DeltaNet), split by head
+        if cfg.full_attn_interval:
+            assert cfg.ssm_k_heads % W == 0 and cfg.ssm_v_heads % W == 0
+        self.nk_loc, self.nv_loc = cfg.ssm_k_heads // W, cfg.ssm_v_heads // W
+        if cfg.n_experts and tp is not None:
+            assert cfg.n_experts % W == 0 and cfg.shared_expert_ffn % W == 0
         self.device = torch.device(device)
         lo, hi = layer_range or (0, cfg.n_layers)
         self.lo, self.hi = lo, hi
@@ -120,9 +131,8 @@ class LlamaGPU:
                 n_attn += 1
                 d = cfg.head_dim
                 qh = 2 * d if cfg.attn_output_gate else d
-                shares = ((tr * self.n_q * qh, (tr + 1) * self.n_q * qh),
-                          (tr * self.n_kv * d, (tr + 1) * self.n_kv * d),
-                          (tr * self.n_kv * d, (tr + 1) * self.n_kv * d))
+                kv_rows = (self.kv0 * d, (self.kv0 + self.n_kv) * d)
+                shares = ((tr * self.n_q * qh, (tr + 1) * self.n_q * qh), kv_rows, kv_rows)
                 rows = sum(z - a for a, z in shares)
                 if cfg.fused_qkv:  # one q|k|v tensor: each part's rows at its offset
                     t, qt, shape = get(b + "attn_qkv.weight")
@@ -205,21 +215,40 @@ class LlamaGPU:
 
     def _load_deltanet(self, L, b, get, small):
         """Gated DeltaNet layer: in-projection (q|k|v), z gate, beta/decay
-        projection, conv1d, decay parameters, gated norm, out-projection."""
+        projection, conv1d, decay parameters, gated norm, out-projection.
+        Under tensor parallelism a rank holds nk/W key heads and the nv/W
+        value heads that read them: its rows of q, k, v, z, beta and alpha,
+        its conv channels and decay parameters, and its K-slice of the
+        out-projection (row-parallel, reduced with the other ranks)."""
         cfg, dev, H = self.cfg, self.device, self.cfg.hidden
-        nv, dh = cfg.ssm_v_heads, cfg.ssm_head_dim
+        nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
+        W, tr = (self.tp.world, self.tp.rank) if self.tp else (1, 0)
+        nkl, nvl = self.nk_loc, self.nv_loc
+        # channel ranges of this rank in the [q | k | v] projection / conv
+        ch = [(tr * nkl * dh, (tr + 1) * nkl * dh),
+              (nk * dh + tr * nkl * dh, nk * dh + (tr + 1) * nkl * dh),
+              (2 * nk * dh + tr * nvl * dh, 2 * nk * dh + (tr + 1) * nvl * dh)]
+
+        def rows_of(t, qt, shape, ranges):
+            return t if W == 1 else torch.cat([split_rows(t, qt, shape, a, z) for a, z in ranges])
         t, qt, shape = get(b + "attn_qkv.weight")
-        L.w_in = QLinear(t, qt, shape[0], H, dev)
+        L.w_in = QLinear(rows_of(t, qt, shape, ch), qt, (2 * nkl + nvl) * dh, H, dev)
         t, qt, shape = get(b + "attn_gate.weight")
-        L.w_z = QLinear(t, qt, shape[0], H, dev)
+        L.w_z = QLinear(rows_of(t, qt, shape, [(tr * nvl * dh, (tr + 1) * nvl * dh)]), qt,
+                        nvl * dh, H, dev)
         t, qt, shape = get(b + "ssm_ba.weight")
-        L.w_ba = QLinear(t, qt, 2 * nv, H, dev, f32_as_f16=True)
-        L.conv_w = small(b + "ssm_conv1d.weight").contiguous()
-        L.dt_bias = small(b + "ssm_dt.bias")
-        L.A = small(b + "ssm_a")
+        L.w_ba = QLinear(rows_of(t, qt, shape, [(tr * nvl, (tr + 1) * nvl),
+                                                (nv + tr * nvl, nv + (tr + 1) * nvl)]),
+                         qt, 2 * nvl, H, dev, f32_as_f16=True)
+        conv = small(b + "ssm_conv1d.weight")
+        L.conv_w = (conv if W == 1 else torch.cat([conv[a:z] for a, z in ch])).contiguous()
+        L.dt_bias = small(b + "ssm_dt.bias")[tr * nvl:(tr + 1) * nvl].contiguous()
+        L.A = small(b + "ssm_a")[tr * nvl:(tr + 1) * nvl].contiguous()
         L.ssm_norm = small(b + "ssm_norm.weight")
         t, qt, shape = get(b + "ssm_out.weight")
-        L.w_out = QLinear(t, qt, H, nv * dh, dev)
+        if W > 1:
+            t = split_cols(t, qt, shape, tr * nvl * dh, (tr + 1) * nvl * dh)
+        L.w_out = QLinear(t, qt, H, nvl * dh, dev)
 
     def linear_state_spec(self):
         """(n_layers, nv, dk, dv, conv_channels, conv_k) of this stage's
@@ -227,8 +256,8 @@ class LlamaGPU:
         if not self.n_lin_layers:
             return None
         c = self.cfg
-        return (self.n_lin_layers, c.ssm_v_heads, c.ssm_head_dim, c.ssm_head_dim,
-                (2 * c.ssm_k_heads + c.ssm_v_heads) * c.ssm_head_dim, c.ssm_conv_kernel)
+        return (self.n_lin_layers, self.nv_loc, c.ssm_head_dim, c.ssm_head_dim,
+                (2 * self.nk_loc + self.nv_loc) * c.ssm_head_dim, c.ssm_conv_kernel)
 
     def _load_moe(self, L, b, get, small):
         """Routed experts (+ router, + shared expert) of one layer."""
@@ -243,7 +272,7 @@ class LlamaGPU:
             biases = dict(gate_b=small(b + "ffn_gate_exps.bias").cpu(),
                           up_b=small(b + "ffn_up_exps.bias").cpu(),
                           down_b=small(b + "ffn_down_exps.bias").cpu())
-        ep = self.ep
+        ep = self.ep or self.tp   # experts split over the EP group or the TP group
         shard = dict(e0=ep.rank * (E // ep.world), n_local=E // ep.world) if ep else {}
         L.experts = MoeExperts(g[0].view(E, F, rb_h), u[0].view(E, F, rb_h),
                                d[0].view(E, H, rb_f), qt, H, F, dev, **shard,
@@ -255,11 +284,25 @@ class LlamaGPU:
         L.router_b = small(b + "ffn_gate_inp.bias") if cfg.arch == "gpt-oss" else None
         L.sh_gu = L.sh_down = L.sh_gate = None
         if cfg.shared_expert_ffn:
-            S = cfg.shared_expert_ffn
+            W, tr = (self.tp.world, self.tp.rank) if self.tp else (1, 0)
             gs, us = get(b + "ffn_gate_shexp.weight"), get(b + "ffn_up_shexp.weight")
-            L.sh_gu = QLinear(torch.cat([gs[0], us[0]]), gs[1], 2 * S, H, dev)
+            dq_t = get(b + "ffn_down_shexp.weight")[1]
+            if W > 1 and cfg.shared_expert_ffn % (Q.BLOCK[dq_t][0] * W):
+                # too narrow to split into whole quant blocks: rank 0 runs it alone
+                W, tr = 1, 0
+                if self.tp.rank != 0:
+                    L.sh_gu = L.sh_down = L.sh_gate = None
+                    return
+            S = cfg.shared_expert_ffn // W      # under TP: this rank's features
+            gp, up = gs[0], us[0]
+            if W > 1:
+                gp = split_rows(gs[0], gs[1], gs[2], tr * S, (tr + 1) * S)
+                up = split_rows(us[0], us[1], us[2], tr * S, (tr + 1) * S)
+            L.sh_gu = QLinear(torch.cat([gp, up]), gs[1], 2 * S, H, dev)
             t, qt2, shape = get(b + "ffn_down_shexp.weight")
-            L.sh_down = QLinear(t, qt2, shape[0], shape[1], dev)
+            if W > 1:
+                t = split_cols(t, qt2, shape, tr * S, (tr + 1) * S)
+            L.sh_down = QLinear(t, qt2, shape[0], S, dev)
             t, qt3, _ = get(b + "ffn_gate_inp_shexp.weight")
             L.sh_gate = QLinear(t, qt3, 1, H, dev, f32_as_f16=True)
 
@@ -331,7 +374,7 @@ class LlamaGPU:
     def _deltanet(self, L, b, kv, ctx, x, N):
         """Gated DeltaNet token mixing of one layer -> ctx.ssm_out (fp16)."""
         cfg = self.cfg
-        nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
+        nk, nv, dh = self.nk_loc, self.nv_loc, cfg.ssm_head_dim
         S = b.ssm_seqs.shape[0]
         g = L.w_in(x, ctx.gemm)
         C().ssm_conv_silu(g, L.conv_w, kv.conv_state(L.lin_idx), b.ssm_seqs, S, ctx.ssm_qkv[:N])
@@ -356,7 +399,9 @@ class LlamaGPU:
             if L.experts is not None:
                 # router GEMM + top-k, then plan/scatter/2 grouped GEMMs/combine, or under
                 # expert parallelism send-counts/dispatch/wait/plan/2 GEMMs/wait/combine
-                n += 2 + (8 if self.ep is not None else 5) + (4 if L.sh_gu is not None else 0)
+                # (tensor parallelism: localize/plan/scatter/2 GEMMs/partial store/reduce)
+                n += 2 + (8 if self.ep is not None else 7 if self.tp is not None else 5) + \
+                    (4 if L.sh_gu is not None else 0)
             else:
                 n += 4   # gate|up GEMM, SwiGLU, down GEMM, residual+norm
         if self.last:
@@ -396,8 +441,8 @@ class LlamaGPU:
                 with P("delta_rule"):
                     self._deltanet(L, b, kv, ctx, x, N)
                 with P("o_proj+norm"):
-                    g = L.w_out(ctx.ssm_out[:N], ctx.gemm)
-                    C().epi_residual_rmsnorm(g, h, None, L.ffn_norm, x, cfg.rms_eps)
+                    g = self._row_parallel(L.w_out, ctx.ssm_out[:N], ctx)
+                    self._residual_norm(g, h, None, L.ffn_norm, x, ctx)
             else:
                 li = self.kv_off + L.kv_idx
                 with P("qkv_proj+rope+kv_append"):
@@ -432,12 +477,15 @@ class LlamaGPU:
                               cfg.moe_softmax_after_topk)
                     sh = shg = None
                     if L.sh_gu is not None:
-                        S = cfg.shared_expert_ffn
+                        S = L.sh_gu.rows // 2
                         g = L.sh_gu(x, ctx.gemm)
                         C().epi_swiglu(g, None, S, 0, False, 0.0, 0.0, ctx.act_sh[:N])
                         shg = L.sh_gate(x, ctx.gemm_side)
                         sh = L.sh_down(ctx.act_sh[:N], ctx.gemm)
-                    if self.ep is not None:
+                    if self.tp is not None:
+                        g = moe_experts_tp(x, L.experts, ctx.moe, self.tp, sh, shg)
+                        self._residual_norm(g, h, None, nxt_w, nxt_out, ctx)
+                    elif self.ep is not None:
                         moe_experts_ep(x, L.experts, ctx.moe, self.ep, h, nxt_w, nxt_out, cfg.rms_eps,
                                        sh, shg)
                     else:
@@ -524,7 +572,7 @@ class GpuForwardContext:
             self.gate = torch.zeros(max_tokens, model.n_q * cfg.head_dim, dtype=torch.float16,
                                     device=dev)
         if model.n_lin_layers:
-            nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
+            nk, nv, dh = model.nk_loc, model.nv_loc, cfg.ssm_head_dim
             self.ssm_qkv = torch.zeros(max_tokens, (2 * nk + nv) * dh, dtype=torch.float32,
                                        device=dev)
             self.ssm_out = torch.zeros(max_tokens, nv * dh, dtype=torch.float16, device=dev)
@@ -565,6 +613,7 @@ class LlamaCPU:
         # KV caches are stage-local: layer lo of this stage is cache layer 0.
         self.kv_off = 0 if kv_layer_offset is None else kv_layer_offset
         self.dtype = dtype
+        self.nk_loc, self.nv_loc = cfg.ssm_k_heads, cfg.ssm_v_heads
 
         def dq(name):
             t, qt, shape = source.get(name)

@@ -187,6 +187,30 @@ def moe_experts_ep(x: torch.Tensor, experts: MoeExperts, ws: "MoeWorkspace", ep,
     c.moe_combine(ep.comb, ws.wts, k, shared, shared_gate, residual, norm_w, out, eps)
 
 
+def moe_experts_tp(x: torch.Tensor, experts: MoeExperts, ws: MoeWorkspace, tp, shared=None,
+                   shared_gate=None):
+    """The experts under tensor parallelism (parallel/tp.py): every rank of the
+    group holds every token and experts [e0, e0 + n_local); it runs its own
+    (token, k) pairs only and stores its share of the output into the column
+    owners' buffers.  Returns the GemmOut that tp.reduce_norm sums."""
+    T = x.shape[0]
+    k = ws.k
+    P = T * k
+    c = C()
+    ex = experts
+    c.moe_localize(ws.ids[:P], ws.wts[:P], ws.counts, ws.E, ex.e0, ex.n_local)
+    N = int(c.moe_tok_tile(P, ex.n_local))
+    c.moe_plan(ws.counts, ex.n_local, N, ws.offsets, ws.cursor, ws.tiles, ws.n_tiles, ws.status)
+    c.moe_scatter(x, ws.ids[:P], k, ws.cursor, ws.xs, ws.ret, 0)
+    c.moe_gemm(ex.fmt, EPI_SWIGLU, ex.w_gu, 2 * ex.F, ex.H, ws.xs, N, ws.tiles, ws.n_tiles,
+               ex.b_gu, 2 * ex.F, ws.h, ex.act_kind, ex.alpha, ex.limit, [], 0, None,
+               ws.num_sms, ws.status)
+    c.moe_gemm(ex.fmt, EPI_STORE, ex.w_down, ex.H, ex.F, ws.h, N, ws.tiles, ws.n_tiles,
+               ex.b_down, ex.H, None, 0, 0.0, 0.0, [ws.rows.data_ptr()], ex.H, ws.ret,
+               ws.num_sms, ws.status)
+    return tp.moe_partial(ws.rows, ws.wts, k, shared, shared_gate, T)
+
+
 def moe_ffn(x, experts, router, router_b, ws, gemm, residual, norm_w, out, eps,
             softmax_after_topk: bool = True, shared=None, shared_gate=None):
     """Routing + experts + combine in one call (no shared expert between)."""

@@ -113,6 +113,18 @@ class TpGroup:
                                    self.ws_bytes // 4, dsts, self.ctl[4 * b:], self.bases,
                                    self.flag_off + b * W * 4, r, owner_tiles)
 
+    def moe_partial(self, rows, wts, k: int, shared, shared_gate, T: int):
+        """This rank's MoE output (its experts, its slice of the shared
+        expert) stored into the column owners' receive slots, like a
+        row-parallel GEMM's partials; reduce_norm sums them next."""
+        b = self.k & 1
+        W, r = self.world, self.rank
+        own = self.base + (b * W) * self.ws_bytes
+        dsts = [self.bases[o] + (b * W + r) * self.ws_bytes for o in range(W)]
+        return C().moe_combine_tp(rows, wts, k, shared, shared_gate, T, self.H, own,
+                                  self.ws_bytes // 4, dsts, self.ctl[4 * b:], self.bases,
+                                  self.flag_off + b * W * 4, r)
+
     def reduce_norm(self, g, bias, w, out, eps: float, status: torch.Tensor, num_sms: int):
         """Residual += sum over ranks of the row-parallel result (+ bias), then
         out = RMSNorm(residual) * w; the residual ends up replicated."""

@@ -69,10 +69,21 @@ class _TablesView:
 
 
 class _BroadcastingRunner:
-    """The root's runner: sends the step to the other ranks, then runs it."""
+    """The root's runner: sends the step to the other ranks, then runs it.
+    Recurrent-state slots the root frees (hybrid models) travel with the next
+    step, so every rank keeps the same slot table."""
 
     def __init__(self, eng: "TpEngine", inner):
         self._eng, self._inner = eng, inner
+        self.released: list[int] = []
+        if inner.slots is not None:
+            real = inner.slots.release
+
+            def release(sid):
+                if sid in inner.slots.of:
+                    self.released.append(int(sid))
+                real(sid)
+            inner.slots.release = release
 
     def __getattr__(self, name):
         return getattr(self._inner, name)
@@ -102,6 +113,9 @@ class TpEngine(LLMEngine):
         cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=timeout_s))
         model = LlamaGPU(cfg, source_factory(), dev, tp=tpg)
         ecfg = EngineConfig(**{**ecfg.__dict__})
+        if model.n_lin_layers:
+            # saved recurrent states (hybrid prefix hits) are copied on the root only
+            ecfg.prefix_cache = False
         if not ecfg.kv_pages:  # the same page count everywhere: the minimum over the ranks
             free, _ = torch.cuda.mem_get_info(dev)
             from ..ops.attention import PagedKVCache
@@ -127,12 +141,14 @@ class TpEngine(LLMEngine):
     def _send_step(self, plan, bt_seq: np.ndarray, use_graph: bool):
         N, B = len(plan.tokens), len(plan.seq_ids)
         mp = self.runner._inner.max_pages
-        hdr = torch.tensor([_STEP, N, B, mp, int(plan.n_prefill_tokens), int(use_graph), 0, 0],
+        rel = self.runner.released
+        self.runner.released = []
+        hdr = torch.tensor([_STEP, N, B, mp, int(plan.n_prefill_tokens), int(use_graph), len(rel), 0],
                            dtype=torch.int64)
         self._bcast(hdr)
         body = np.concatenate([np.asarray(a, np.int64).reshape(-1) for a in (
             plan.tokens, plan.positions, plan.slots, plan.row_seq, plan.seq_ids, plan.seq_start,
-            plan.seq_ntok, plan.seq_sample, bt_seq)])
+            plan.seq_ntok, plan.seq_sample, bt_seq, rel)])
         self._bcast(torch.from_numpy(np.ascontiguousarray(body, dtype=np.int32)))
 
     def stop(self):
@@ -175,7 +191,8 @@ class TpEngine(LLMEngine):
                     torch.cuda.synchronize(self.device)
                     on_replay(ev[0].elapsed_time(ev[1]))
                 continue
-            body = torch.zeros(4 * N + 4 * B + B * mp, dtype=torch.int32)
+            n_rel = rb    # header slot 6: recurrent-state slots the root released
+            body = torch.zeros(4 * N + 4 * B + B * mp + n_rel, dtype=torch.int32)
             self._bcast(body)
             b = body.numpy()
             o = 0
@@ -188,6 +205,9 @@ class TpEngine(LLMEngine):
             tokens, positions, slots, row_seq = take(N), take(N), take(N), take(N)
             seq_ids, seq_start, seq_ntok, seq_samp = take(B), take(B), take(B), take(B)
             bt_seq = take(B * mp).reshape(B, mp)
+            if n_rel and runner.slots is not None:
+                for sid in take(n_rel).tolist():
+                    runner.slots.release(int(sid))
             plan = _PlanView(tokens, positions, slots, row_seq, seq_ids, seq_start, seq_ntok,
                              seq_samp, n_pf)
             n_samp = int(np.sum(seq_samp))

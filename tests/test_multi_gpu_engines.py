@@ -32,6 +32,33 @@ def _cfg():
                        embed_qtype="F16", output_qtype="Q4_K")
 
 
+def _hybrid_cfg():
+    """Qwen3-Next-like: gated DeltaNet + gated attention (2 KV heads: replicated
+    at TP4), 8 experts top-2 with a shared expert."""
+    from swarmllm_b200.models.config import ModelConfig
+    return ModelConfig(name="t-hybrid", arch="qwen3next", n_layers=4, hidden=512, n_heads=4,
+                       n_kv_heads=2, head_dim=256, ffn=512, vocab=1024, rope_theta=1e7,
+                       rope_neox=True, rope_dim=64, rms_eps=1e-6, qk_norm=True,
+                       attn_output_gate=True, n_experts=8, n_experts_used=2, expert_ffn=256,
+                       shared_expert_ffn=512, moe_softmax_after_topk=True,
+                       full_attn_interval=4, ssm_k_heads=2, ssm_v_heads=8, ssm_head_dim=128,
+                       ssm_conv_kernel=4, weight_qtype="Q4_K", embed_qtype="F16",
+                       output_qtype="Q4_K", expert_qtype="Q4_K")
+
+
+def _moe_cfg():
+    """Qwen3-MoE-like dense attention with q/k norms and routed experts."""
+    from swarmllm_b200.models.config import ModelConfig, apply_family
+    return apply_family(ModelConfig(name="t-moe", arch="qwen3moe", n_layers=3, hidden=512,
+                                    n_heads=8, n_kv_heads=4, head_dim=64, ffn=512, vocab=1024,
+                                    n_experts=8, n_experts_used=2, expert_ffn=256,
+                                    weight_qtype="Q4_K", embed_qtype="F16", output_qtype="Q4_K",
+                                    expert_qtype="Q4_K"))
+
+
+_CFGS = {"dense": None, "hybrid": _hybrid_cfg, "moe": _moe_cfg}
+
+
 def _prompts(cfg):
     rng = np.random.default_rng(11)
     return [rng.integers(0, cfg.vocab, n).tolist() for n in PROMPT_LENS]
@@ -43,12 +70,15 @@ def _ecfg():
                         kv_pages=128, graph_sizes=(1, 2, 4, 8), prefix_cache=False)
 
 
-def _reference():
-    """Single-GPU engine: greedy tokens and the first step's logits."""
+def _reference(kind="dense"):
+    """Single-GPU engine: greedy tokens."""
     from swarmllm_b200.engine import LLMEngine, SamplingParams
     from swarmllm_b200.models.weights import RandomSource
-    cfg = _cfg()
-    eng = LLMEngine.from_config(cfg, "cuda:0", _ecfg(), source=RandomSource(cfg, seed=7))
+    cfg = (_CFGS[kind] or _cfg)()
+    ec = _ecfg()
+    if cfg.full_attn_interval:
+        ec.prefix_cache = False
+    eng = LLMEngine.from_config(cfg, "cuda:0", ec, source=RandomSource(cfg, seed=7))
     outs = eng.generate(_prompts(cfg), SamplingParams(max_tokens=GEN))
     return [o.token_ids for o in outs]
 
@@ -80,14 +110,14 @@ def _init(rank, world, port):
     return dev
 
 
-def _tp_worker(rank, world, port, q):
+def _tp_worker(rank, world, port, q, kind="dense"):
     import torch.distributed as dist
     from swarmllm_b200.engine import SamplingParams
     from swarmllm_b200.models.weights import RandomSource
     from swarmllm_b200.parallel.tp_engine import TpEngine
     _init(rank, world, port)
     try:
-        cfg = _cfg()
+        cfg = (_CFGS[kind] or _cfg)()
         eng = TpEngine.create(cfg, _ecfg(), lambda: RandomSource(cfg, seed=7))
         if eng.root:
             outs = eng.generate(_prompts(cfg), SamplingParams(max_tokens=GEN))
@@ -125,12 +155,24 @@ def _spawn(fn, world, timeout=600):
     return got
 
 
+def _tp_hybrid_worker(rank, world, port, q):
+    _tp_worker(rank, world, port, q, "hybrid")
+
+
+def _tp_moe_worker(rank, world, port, q):
+    _tp_worker(rank, world, port, q, "moe")
+
+
+@pytest.mark.parametrize("kind", ["dense", "hybrid", "moe"])
 @pytest.mark.parametrize("world", [2, 4])
-def test_tp_engine_matches_single_gpu(world):
+def test_tp_engine_matches_single_gpu(world, kind):
+    """TP over dense, hybrid (DeltaNet heads, gated attention with replicated
+    KV heads at TP4, experts + shared expert) and MoE models."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    want = _reference()
-    got, got2, status = _spawn(_tp_worker, world)
+    want = _reference(kind)
+    fn = {"dense": _tp_worker, "hybrid": _tp_hybrid_worker, "moe": _tp_moe_worker}[kind]
+    got, got2, status = _spawn(fn, world)
     assert status[0] == 0, status
     _check(got, want)
     _check(got2, want[:1])
