@@ -22,6 +22,11 @@ stage's tensor-parallel group, stage 0 lanes get the header and plan by a
 broadcast from the root; other stages' lanes receive them from the previous
 stage's same lane.
 
+A long prompt is prefilled in chunks (the scheduler's prefill_chunk); a chunk
+that samples nothing is committed as soon as it is sent, so the wave's next
+chunk follows it down the chain and up to one chunk per stage is in flight:
+the stages prefill one prompt together instead of in turn.
+
 Reference: the reference pipelines a prompt's chunks through every segment
 at once (pipeline/prompt_chunks.rs) and keeps several requests in flight on a
 split model; one request's tokens still go one at a time through the chain.
@@ -109,6 +114,7 @@ class AsyncPipelineEngine:
         self.comm_dev = self.device if self.gpu else torch.device("cpu")
         self._pending = deque()
         self.retired = 0  # wave steps completed (root)
+        self.chunks_pipelined = 0  # prompt chunks sent behind another of their wave (root)
 
     # ------------------------------------------------------------------ requests (root)
     def add_request(self, prompt_ids, params: SamplingParams | None = None) -> int:
@@ -251,17 +257,25 @@ class AsyncPipelineEngine:
         the oldest wave in flight.  Returns (request id, token, finished) events."""
         events = []
         for v in range(self.V):
-            if not issue or busy[v] or not self.scheds[v].has_work():
-                continue
-            plan = self.scheds[v].schedule()
-            if len(plan) == 0:
-                continue
-            hdr, body = self._pack(v, plan)
-            if self.tp > 1:
-                self._tp_bcast(hdr, body)
-            res = self._stage_step(hdr, body, None)
-            busy[v] = True
-            inflight.append((v, plan, res))
+            chunks = 0
+            while issue and not busy[v] and self.scheds[v].has_work() and chunks < self.S:
+                plan = self.scheds[v].schedule()
+                if len(plan) == 0:
+                    break
+                hdr, body = self._pack(v, plan)
+                if self.tp > 1:
+                    self._tp_bcast(hdr, body)
+                res = self._stage_step(hdr, body, None)
+                if int(np.sum(plan.seq_sample)) == 0:
+                    # A prompt chunk that samples nothing returns nothing: commit it
+                    # now and send the wave's next chunk right behind it, so a long
+                    # prompt's chunks fill the stages at once (up to one per stage).
+                    self.scheds[v].commit(plan, [])
+                    self.chunks_pipelined += 1
+                    chunks += 1
+                    continue
+                busy[v] = True
+                inflight.append((v, plan, res))
         if not inflight:
             return events
         v, plan, res = inflight.popleft()

@@ -32,7 +32,7 @@ def test_stage_bounds():
     assert stage_bounds(2, 2) == [0, 1, 2]
 
 
-def _async_worker(rank, world, port, q):
+def _async_worker(rank, world, port, q, long_prompt=False):
     import os
     import torch
     import torch.distributed as dist
@@ -50,10 +50,11 @@ def _async_worker(rank, world, port, q):
                         prefix_cache=False)
     eng = AsyncPipelineEngine(cfg, ecfg, lambda: RandomSource(cfg, seed=5), "cpu")
     rng = np.random.default_rng(4)
-    prompts = [rng.integers(0, cfg.vocab, n).tolist() for n in (5, 30, 12, 21, 9)]
+    lens = (60,) if long_prompt else (5, 30, 12, 21, 9)
+    prompts = [rng.integers(0, cfg.vocab, n).tolist() for n in lens]
     out = eng.generate(prompts, SamplingParams(max_tokens=9, ignore_eos=True))
     if rank == 0:
-        q.put(out)
+        q.put((out, eng.chunks_pipelined) if long_prompt else out)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -93,3 +94,45 @@ def test_async_waves_match_single_process(world):
             if p.is_alive():
                 p.kill()
     assert got == want
+
+
+def _async_long_worker(rank, world, port, q):
+    _async_worker(rank, world, port, q, long_prompt=True)
+
+
+def test_async_prompt_chunks_flow_through_stages():
+    """One 60-token prompt in 16-token chunks over 3 stages: the chunks that
+    sample nothing go down the chain one behind the other (not one at a time
+    through every stage), and the output equals one process."""
+    import multiprocessing as mp
+    import socket
+    from swarmllm_b200.engine import EngineConfig, LLMEngine, SamplingParams
+    from swarmllm_b200.models.config import tiny_llama
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = tiny_llama().scaled(n_layers=3)
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(0, cfg.vocab, 60).tolist()]
+    ref = LLMEngine.from_config(cfg, "cpu", EngineConfig(max_model_len=128, max_running=6,
+                                                         max_step_tokens=64, prefill_chunk=16,
+                                                         prefix_cache=False),
+                                source=RandomSource(cfg, seed=5))
+    want = [o.token_ids for o in ref.generate(prompts, SamplingParams(max_tokens=9,
+                                                                      ignore_eos=True))]
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_async_long_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    try:
+        got, pipelined = q.get(timeout=240)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert got == want
+    assert pipelined >= 2      # chunks 2 and 3 of 4 followed the one before them
