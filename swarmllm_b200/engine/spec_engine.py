@@ -8,7 +8,9 @@ the CLI and the benchmarks can serve a model with a drafter.
 Each ``step()`` admits waiting requests (prefill of target and drafter; the
 first token is sampled from the prefill), then runs one speculative round for
 every running request: a draft tree of `spec_depth` levels x `spec_width`
-children from the drafter model (engine/spec.py), or an n-gram chain looked up
+children from the drafter model (engine/spec.py) -- a drafter preset or GGUF,
+the target itself ("self"), or the target with a block of middle layers
+skipped ("swift[:ratio]", engine/swift.py) -- or an n-gram chain looked up
 in the request's own text when ``draft_model == "ngram"`` (engine/ngram_spec.py),
 verified by one target forward.  A step reports every token it committed, so
 a request can advance several tokens per step.  Greedy and sampled requests
@@ -136,6 +138,10 @@ class SpecEngine:
         else:
             if ecfg.draft_model == "self":      # the target drafts for itself: acceptance bound
                 drafter = target
+            elif ecfg.draft_model.startswith("swift"):  # "swift" or "swift:<skip ratio>"
+                from .swift import layer_skip_drafter, skip_patterns
+                ratio = float(ecfg.draft_model.split(":", 1)[1]) if ":" in ecfg.draft_model else 0.45
+                drafter = layer_skip_drafter(target, skip_patterns(len(target.layers), ratio)[0])
             elif ecfg.draft_model.endswith(".gguf") or "/" in ecfg.draft_model:
                 from ..models.weights import GgufSource
                 dsrc = GgufSource(ecfg.draft_model)

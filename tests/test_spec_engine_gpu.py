@@ -89,3 +89,17 @@ def test_spec_engine_serves_http():
         assert r.status_code == 200, r.text
         assert r.json()["usage"]["completion_tokens"] == 12
     ae.shutdown()
+
+
+def test_spec_engine_swift_layer_skip():
+    """The target drafting with a middle block of its layers skipped: output
+    is the target's own."""
+    from swarmllm_b200.engine import SamplingParams
+    cfg = _cfg(layers=6)
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, cfg.vocab, n).tolist() for n in (15, 33)]
+    sp = SamplingParams(max_tokens=16)
+    want = _plain(cfg, prompts, sp)
+    got, eng = _spec(cfg, prompts, sp, "swift:0.34")
+    assert eng.dec.d.model.skipped == 2 and len(eng.dec.d.model.layers) == 4
+    assert _agree(got, want) >= 0.95, (got, want)
