@@ -34,6 +34,7 @@ split model; one request's tokens still go one at a time through the chain.
 from __future__ import annotations
 
 import itertools
+import time
 from collections import deque
 
 import numpy as np
@@ -56,7 +57,9 @@ class AsyncPipelineEngine:
     segments_served = 0    # layer-range forwards this rank ran (swarmllm_segments_served_total)
     bytes_sent = 0         # bytes this rank sent to other ranks (swarmllm_network_bytes_total)
     def __init__(self, cfg: ModelConfig, ecfg: EngineConfig, source_factory, device,
-                 tp: int = 1, waves: int | None = None):
+                 tp: int = 1, waves: int | None = None, bounds: list | None = None):
+        """`bounds`: layer boundaries [stages + 1] (default: the layout planner's
+        cut over its per-layer costs; the rebalancer passes measured ones)."""
         self.cfg, self.ecfg = cfg, ecfg
         self.rank, self.world = dist.get_rank(), dist.get_world_size()
         assert self.world % tp == 0
@@ -65,8 +68,9 @@ class AsyncPipelineEngine:
         self.device = torch.device(device)
         self.gpu = self.device.type == "cuda"
         from .planner import layer_costs
-        self.bounds = stage_bounds(cfg.n_layers, self.S,
-                                   costs=layer_costs(cfg, max(1, ecfg.max_running), 2048, tp))
+        self.bounds = list(bounds) if bounds is not None else stage_bounds(
+            cfg.n_layers, self.S, costs=layer_costs(cfg, max(1, ecfg.max_running), 2048, tp))
+        assert len(self.bounds) == self.S + 1 and self.bounds[-1] == cfg.n_layers
         lo, hi = self.bounds[self.stage], self.bounds[self.stage + 1]
         self.lo, self.hi = lo, hi
         self.root = self.rank == 0
@@ -113,6 +117,7 @@ class AsyncPipelineEngine:
             self._ids = itertools.count()
         self.comm_dev = self.device if self.gpu else torch.device("cpu")
         self._pending = deque()
+        self.stage_s = 0.0  # moving average of this stage's forward time (rebalancer)
         self.retired = 0  # wave steps completed (root)
         self.chunks_pipelined = 0  # prompt chunks sent behind another of their wave (root)
 
@@ -193,7 +198,12 @@ class AsyncPipelineEngine:
             grp = attention_groups(None, self.cfg.n_heads // self.cfg.n_kv_heads, seq_start, seq_ntok)
             if grp is not None:
                 batch.groups = (t(grp[0]), t(grp[1]), grp[2])
+        t0 = time.perf_counter()
         out = self.model.forward(batch, self.kv, self.ctx, h_in)
+        if self.gpu:
+            torch.cuda.current_stream(self.device).synchronize()
+        self.stage_s = 0.8 * self.stage_s + 0.2 * (time.perf_counter() - t0) \
+            if self.stage_s else time.perf_counter() - t0
         self.segments_served += 1
         return out, positions[samp_rows] if len(samp_rows) else positions[:0]
 

@@ -106,6 +106,7 @@ class ResilientPipeline:
         self.epoch = 0
         self.build_engine = build_engine
         self.recoveries = 0
+        self.rebalances = 0
         self.outliers = outliers or OutlierTracker()
         self._suspects: list[int] = []     # stale ranks seen by the root before a recovery
         self._form_group()
@@ -208,6 +209,30 @@ class ResilientPipeline:
                 if self.recoveries >= max_recoveries:
                     raise
                 self._recover()
+
+    def rebalance(self, rebalancer, stage_s: list | None = None) -> bool:
+        """Collective: gather every stage's measured step time (or use
+        `stage_s`), let the root ask `rebalancer` (parallel/rebalance.py) for
+        a better cut, and rebuild every rank's engine with it.  `build_engine`
+        must accept `bounds=`.  Returns whether the layers moved."""
+        times = [None] * len(self.members)
+        dist.all_gather_object(times, getattr(self.eng, "stage_s", 0.0))
+        key = f"rebalance/{self.epoch}/{self.rebalances}"
+        if self.root:
+            S = getattr(self.eng, "S", getattr(self.eng, "n_stages", 1))
+            per_stage = stage_s or [max(times[i] for i in range(len(times))
+                                        if i // self.eng.tp == s) for s in range(S)]
+            new = rebalancer.propose(self.eng.bounds, per_stage)
+            self.store.set(key, ",".join(map(str, new)) if new else "")
+        self.store.wait([key])
+        val = self.store.get(key).decode()
+        self.rebalances += 1
+        if not val:
+            return False
+        bounds = [int(x) for x in val.split(",")]
+        dist.barrier()
+        self.eng = self.build_engine(bounds=bounds)
+        return True
 
     def close(self):
         try:
