@@ -191,8 +191,13 @@ struct MCfg {
   static constexpr int U = DQ;
   static constexpr int THREADS = 96 + 128 * DQ;
   static constexpr int FIRST_DQ_WARP = 3;
-  static constexpr int A_COL = 512 - 128 * U;  // two accumulators below it
-  static_assert(A_COL >= 2 * N, "TMEM budget");
+  static constexpr int A_COL = 512 - 128 * U;  // two accumulator slots below it
+  // Each slot rotates its MMAs over NACC sub-accumulators (summed in the
+  // drain): at decode sizes consecutive MMAs into one accumulator wait for
+  // each other, independent ones overlap.
+  static constexpr int NACC = (A_COL / (2 * N)) >= 4 ? 4 : ((A_COL / (2 * N)) >= 2 ? 2 : 1);
+  static constexpr int SLOT = NACC * N;          // TMEM columns per slot
+  static_assert(A_COL >= 2 * SLOT, "TMEM budget");
   static constexpr int X_UNIT_BYTES = N * 512;
   static constexpr int W_STAGE = FMT == kMoeFmtQ4K ? 128 * kQ4kRowBytes : kMxUnitBytes;
   static constexpr int W_ST = 2 * DQ;
@@ -344,12 +349,12 @@ __global__ void __launch_bounds__(MCfg<N, FMT>::THREADS, 1)
         tc_fence_after();
         const uint64_t xd = xdesc0 + (uint64_t)((s * C::X_UNIT_BYTES) >> 4);
         const uint32_t ab = tmem_base + C::A_COL + s * 128;
-        const uint32_t dt = tmem_base + slot * N;
+        const uint32_t dt = tmem_base + slot * C::SLOT;
         const int nk = (last ? a.last_k : 256) >> 4;
         for (int kk = 0; kk < nk; ++kk)
-          umma_f16_ts(dt, ab + kk * 8,
+          umma_f16_ts(dt + (uint32_t)((kk % C::NACC) * N), ab + kk * 8,
                       xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4), idesc,
-                      (first && kk == 0) ? 0u : 1u);
+                      (first && kk < C::NACC) ? 0u : 1u);
         umma_commit(&empty[s]);
         if (last) umma_commit(&d_full[slot]);
       }
@@ -421,7 +426,7 @@ __global__ void __launch_bounds__(MCfg<N, FMT>::THREADS, 1)
         const int tile = it / RT, rt = it - tile * RT;
         const int4 tinfo = a.tiles[tile];
         const int e = tinfo.x, row0 = tinfo.y, nrows = tinfo.z;
-        const uint32_t dbase = tmem_base + lane_off + slot * N;
+        const uint32_t dbase = tmem_base + lane_off + slot * C::SLOT;
         if constexpr (EPI == kMoeEpiStore) {
           const int rowg = rt * 128 + row;
           const bool valid = rowg < a.rows_valid;
@@ -431,6 +436,15 @@ __global__ void __launch_bounds__(MCfg<N, FMT>::THREADS, 1)
             uint32_t r[16];
             tmem_ld_x16(dbase + c * 16, r);
             tmem_wait_ld();
+#pragma unroll
+            for (int acc = 1; acc < C::NACC; ++acc) {
+              uint32_t r2[16];
+              tmem_ld_x16(dbase + acc * N + c * 16, r2);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                r[e] = __float_as_uint(__uint_as_float(r[e]) + __uint_as_float(r2[e]));
+            }
 #pragma unroll
             for (int q = 0; q < 16; ++q) {
               const int t = c * 16 + q;
@@ -456,6 +470,15 @@ __global__ void __launch_bounds__(MCfg<N, FMT>::THREADS, 1)
             uint32_t r[16];
             tmem_ld_x16(dbase + c * 16, r);
             tmem_wait_ld();
+#pragma unroll
+            for (int acc = 1; acc < C::NACC; ++acc) {
+              uint32_t r2[16];
+              tmem_ld_x16(dbase + acc * N + c * 16, r2);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                r[e] = __float_as_uint(__uint_as_float(r[e]) + __uint_as_float(r2[e]));
+            }
 #pragma unroll
             for (int q = 0; q < 16; q += 2) {
               const float v0 = __uint_as_float(r[q]) + bias, v1 = __uint_as_float(r[q + 1]) + bias;
@@ -702,6 +725,7 @@ int launch_moe_gemm_tc(int fmt, int epi, const void* w, int rows, int K, const v
                        const int32_t* ret, int num_sms, int* status, cudaStream_t s,
                        int* sig_ctl, const unsigned long long* sig_bases, long long sig_flag_off,
                        int sig_world, int sig_rank) {
+  if (K < 64) return -1;  // every item's first unit feeds all (<= 4) sub-accumulators
   if (fmt == kMoeFmtQ4K && K % 256) return -1;
   if (fmt == kMoeFmtMX && K % 64) return -1;  // TMA boxes + the bf16 pair layout
   if (epi == kMoeEpiSwiglu && (rows % 128)) return -1;  // 64 features (gate + up) per tile
