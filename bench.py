@@ -192,6 +192,8 @@ def result_line(cfg, args, m, n_gpus, parallelism, weight_gb, launches_per_step,
     value = B * args.steps / (m["ms_b"] / 1e3)
     headline = cfg.name == "llama-3.3-70b"
     wq = cfg.expert_qtype if cfg.n_experts else cfg.weight_qtype
+    if cfg.quant_mix:
+        wq = f"{wq} + Q6_K ({cfg.quant_mix} mix)"
     b1 = args.steps / (m["ms1"] / 1e3)
     line = {
         "metric": (f"decode tok/s at batch {B} (aggregate), Llama-3.3-70B Q4_K" if headline else

@@ -89,16 +89,18 @@ GemmResult qmatmul_simt(Tensor w, int64_t type, int64_t rows, int64_t K, Tensor 
   return r;
 }
 
-py::tuple q4k_tc_plan_py(int64_t rows, int64_t K, int64_t T, int64_t num_sms) {
+py::tuple q4k_tc_plan_py(int64_t rows, int64_t K, int64_t T, int64_t num_sms, int64_t fmt) {
   int N, ntt, kb, upc, ctas;
   long total;
   size_t need;
-  q4k_tc_plan((int)rows, (int)K, (int)T, (int)num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need);
+  q4k_tc_plan((int)rows, (int)K, (int)T, (int)num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need,
+              (int)fmt);
   return py::make_tuple(N, ntt, kb, total, upc, ctas, need);
 }
 
 GemmResult qgemm_q4k_tc(Tensor w_packed, int64_t rows, int64_t K, Tensor x, Tensor ws,
-                        Tensor status, int64_t num_sms) {
+                        Tensor status, int64_t num_sms, int64_t fmt, OptT w_b, int64_t fmt_b,
+                        int64_t split_tile) {
   CHECK_CUDA(w_packed); CHECK_CUDA(x); CHECK_DT(x, at::kHalf); CHECK_DT(ws, at::kFloat);
   CHECK_DT(status, at::kInt);
   TORCH_CHECK(status.numel() >= 8, "status must hold 8 ints");
@@ -110,7 +112,9 @@ GemmResult qgemm_q4k_tc(Tensor w_packed, int64_t rows, int64_t K, Tensor x, Tens
   int rc = launch_qgemm_q4k_tc(w_packed.data_ptr(), (int)rows, (int)K,
                                reinterpret_cast<const __half*>(x.data_ptr()), (int)x.stride(0), T,
                                ws.data_ptr<float>(), (size_t)ws.numel(), (int)num_sms,
-                               status.data_ptr<int>(), &r.g, cur_stream());
+                               status.data_ptr<int>(), &r.g, cur_stream(), nullptr, 0, nullptr,
+                               nullptr, 0, 0, 0, (int)fmt, ptr_or_null<void>(w_b),
+                               w_b.has_value() ? (int)fmt_b : -1, (int)split_tile);
   TORCH_CHECK(rc == 0, "qgemm_q4k_tc launch failed: rc=", rc);
   r.ws = ws;
   return r;
@@ -150,7 +154,7 @@ GemmResult qgemm_q4k_tc_tp(Tensor w_packed, int64_t rows, int64_t K, Tensor x, T
                            int64_t num_sms, int64_t recv_base, int64_t src_stride,
                            std::vector<int64_t> dst_ptrs, Tensor sig_ctl,
                            std::vector<int64_t> sig_bases, int64_t sig_flag_off, int64_t rank,
-                           int64_t owner_tiles) {
+                           int64_t owner_tiles, int64_t fmt) {
   CHECK_CUDA(w_packed); CHECK_DT(x, at::kHalf); CHECK_DT(status, at::kInt);
   CHECK_DT(sig_ctl, at::kInt);
   TORCH_CHECK(x.size(-1) == K && x.stride(-1) == 1, "x must be [T, K] with unit inner stride");
@@ -170,7 +174,7 @@ GemmResult qgemm_q4k_tc_tp(Tensor w_packed, int64_t rows, int64_t K, Tensor x, T
                                (int)x.size(0), own, (size_t)src_stride, (int)num_sms,
                                status.data_ptr<int>(), &r.g, cur_stream(), d,
                                (int)dst_ptrs.size(), sig_ctl.data_ptr<int>(), b,
-                               (long long)sig_flag_off, (int)rank, (int)owner_tiles);
+                               (long long)sig_flag_off, (int)rank, (int)owner_tiles, (int)fmt);
   TORCH_CHECK(rc == 0, "qgemm_q4k_tc_tp launch failed: rc=", rc);
   r.g.n_src = (int)dst_ptrs.size();
   r.g.src_stride = src_stride;
@@ -213,6 +217,20 @@ void q4k_repack(Tensor src, int64_t rows, int64_t K, Tensor dst) {
   TORCH_CHECK(dst.numel() * dst.element_size() >= rows_pad * (K / 256) * 144, "dst too small");
   const at::cuda::CUDAGuard guard(dst.device());
   TORCH_CHECK(launch_q4k_repack(src.data_ptr(), (int)rows, (int)K, dst.data_ptr(), cur_stream()) == 0,
+              "repack launch failed");
+}
+
+// GGUF Q4_K / Q6_K / Q8_0 rows -> the tiled layout of format `fmt` (qfmt.cuh).
+void qfmt_repack(int64_t fmt, Tensor src, int64_t rows, int64_t K, Tensor dst) {
+  CHECK_CUDA(src); CHECK_CUDA(dst);
+  TORCH_CHECK(fmt >= 0 && fmt <= 2, "unknown format");
+  TORCH_CHECK(K % 256 == 0, "K must be a multiple of 256");
+  const int64_t rows_pad = (rows + 127) / 128 * 128;
+  TORCH_CHECK(dst.numel() * dst.element_size() >= rows_pad * (K / 256) * qfmt_row_bytes((int)fmt),
+              "dst too small");
+  const at::cuda::CUDAGuard guard(dst.device());
+  TORCH_CHECK(launch_qfmt_repack((int)fmt, src.data_ptr(), (int)rows, (int)K, dst.data_ptr(),
+                                 cur_stream()) == 0,
               "repack launch failed");
 }
 
@@ -452,12 +470,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("epi_swiglu", &epi_swiglu);
   m.def("epi_copy", &epi_copy);
   m.def("qmatmul_simt", &qmatmul_simt);
-  m.def("q4k_tc_plan", &q4k_tc_plan_py);
-  m.def("q4k_plan_max_ctas", [](int64_t T, int64_t num_sms) { return q4k_plan_max_ctas((int)T, (int)num_sms); });
+  m.def("q4k_tc_plan", &q4k_tc_plan_py, py::arg("rows"), py::arg("K"), py::arg("T"),
+        py::arg("num_sms"), py::arg("fmt") = 0);
+  m.def("q4k_plan_max_ctas", [](int64_t T, int64_t num_sms, int64_t fmt) {
+    return q4k_plan_max_ctas((int)T, (int)num_sms, (int)fmt); },
+        py::arg("T"), py::arg("num_sms"), py::arg("fmt") = 0);
   m.def("q4k_gemv_max_t", []() { return q4k_gemv_max_t(); });
-  m.def("q4k_gemv_occupancy", [](int64_t T) { return q4k_gemv_occupancy((int)T); });
-  m.def("qgemm_q4k_tc", &qgemm_q4k_tc);
-  m.def("qgemm_q4k_tc_tp", &qgemm_q4k_tc_tp);
+  m.def("q4k_gemv_occupancy", [](int64_t T, int64_t fmt) {
+    return q4k_gemv_occupancy((int)T, (int)fmt); }, py::arg("T"), py::arg("fmt") = 0);
+  m.def("qfmt_of_ggml", [](int64_t t) { return qfmt_of_ggml((int)t); });
+  m.def("qfmt_row_bytes", [](int64_t f) { return qfmt_row_bytes((int)f); });
+  m.def("qfmt_repack", &qfmt_repack);
+  m.def("qgemm_q4k_tc", &qgemm_q4k_tc, py::arg("w_packed"), py::arg("rows"), py::arg("K"),
+        py::arg("x"), py::arg("ws"), py::arg("status"), py::arg("num_sms"), py::arg("fmt") = 0,
+        py::arg("w_b") = py::none(), py::arg("fmt_b") = -1, py::arg("split_tile") = 0);
+  m.def("qgemm_q4k_tc_tp", &qgemm_q4k_tc_tp, py::arg("w_packed"), py::arg("rows"), py::arg("K"),
+        py::arg("x"), py::arg("status"), py::arg("num_sms"), py::arg("recv_base"),
+        py::arg("src_stride"), py::arg("dst_ptrs"), py::arg("sig_ctl"), py::arg("sig_bases"),
+        py::arg("sig_flag_off"), py::arg("rank"), py::arg("owner_tiles"), py::arg("fmt") = 0);
   m.def("tp_reduce_norm", &tp_reduce_norm);
   // Bounded wait for `world` epoch flags (flags: device address of uint32[world]);
   // timeout_ns <= 0 uses the kernels' default deadline (1 s).

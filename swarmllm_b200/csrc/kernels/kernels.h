@@ -36,26 +36,42 @@ void launch_f32_to_f16(const float* x, __half* y, size_t n, cudaStream_t s);
 int launch_qmatmul_simt(const void* w, int type, int rows, int K, const __half* x, int x_stride,
                         int T, float* out, int out_stride, cudaStream_t s);
 int q4k_tc_tok_tile(int T);
+// Weight formats of the repacked quantized GEMM (qfmt.cuh): the GGML type
+// number maps to fmt 0 = Q4_K, 1 = Q6_K, 2 = Q8_0; -1 = no tensor-core path.
+constexpr int qfmt_of_ggml(int ggml_type) {
+  return ggml_type == 12 ? 0 : (ggml_type == 14 ? 1 : (ggml_type == 8 ? 2 : -1));
+}
+constexpr int qfmt_row_bytes(int fmt) { return fmt == 0 ? 144 : (fmt == 1 ? 224 : 272); }
 // Decode at <= kQGemvMaxT tokens runs the CUDA-core GEMV (qgemv_q4k.cu) with
-// q4k_gemv_ctas_per_sm(T) CTAs per SM; the plan below accounts for it.
+// qgemv_ctas_per_sm(fmt, T) CTAs per SM; the plan below accounts for it.
 constexpr int kQGemvMaxT = 2;
-constexpr int q4k_gemv_ctas_per_sm(int T) { return T == 1 ? 5 : 4; }
+constexpr int qgemv_ctas_per_sm(int fmt, int T) {
+  return fmt == 0 ? (T == 1 ? 5 : 4) : (fmt == 1 ? 3 : (T == 1 ? 3 : 2));
+}
+constexpr int q4k_gemv_ctas_per_sm(int T) { return qgemv_ctas_per_sm(0, T); }
 int q4k_gemv_max_t();          // kQGemvMaxT unless SWARMLLM_QGEMV_MAX_T overrides (0 = off)
-int q4k_plan_max_ctas(int T, int num_sms);
-int q4k_gemv_occupancy(int T);  // resident GEMV CTAs per SM (diagnostics)
+int q4k_plan_max_ctas(int T, int num_sms, int fmt = 0);
+int q4k_gemv_occupancy(int T, int fmt = 0);  // resident GEMV CTAs per SM (diagnostics)
 int launch_qgemv_q4k(const void* w_packed, int rows, int K, const __half* x, int x_stride, int T,
                      float* ws, int ksb, long total_units, int upc, int ctas, int* status,
                      const unsigned long long* peer_ws, int n_peers, int* sig_ctl,
                      const unsigned long long* sig_bases, long long sig_flag_off, int sig_rank,
-                     cudaStream_t s, int owner_tiles = 0);
+                     cudaStream_t s, int owner_tiles = 0, int fmt = 0,
+                     const void* w_b = nullptr, int fmt_b = -1, int split_tile = 0);
 void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* ksb,
-                 long* total_units, int* upc, int* n_ctas, size_t* ws_floats);
+                 long* total_units, int* upc, int* n_ctas, size_t* ws_floats, int fmt = 0);
+// fmt selects the repacked weight format (qfmt_of_ggml); the name keeps the
+// format the kernel started with.  Mixed-format GEMM (a Q4_K_M checkpoint's
+// q|k|v, whose v rows are Q6_K): row tiles [0, split_tile) come from w_packed
+// in fmt, the rest from w_b in fmt_b (only fmt Q4_K + fmt_b Q6_K is built).
 int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, int x_stride,
                         int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
                         swarm::GemmOut* out, cudaStream_t s,
                         const unsigned long long* peer_ws = nullptr, int n_peers = 0,
                         int* sig_ctl = nullptr, const unsigned long long* sig_bases = nullptr,
-                        long long sig_flag_off = 0, int sig_rank = 0, int owner_tiles = 0);
+                        long long sig_flag_off = 0, int sig_rank = 0, int owner_tiles = 0,
+                        int fmt = 0, const void* w_b = nullptr, int fmt_b = -1,
+                        int split_tile = 0);
 void qgemm_set_trace(void* buf);
 // Dense fp16 weights on tcgen05 (dense_gemm_tc.cu); same workspace contract.
 void dense_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* kb,
@@ -64,6 +80,8 @@ int launch_dense_gemm_tc(const __half* w, int rows, int K, int w_stride, const _
                          int x_stride, int T, float* ws, size_t ws_floats_avail, int num_sms,
                          int* status, swarm::GemmOut* out, cudaStream_t s);
 int launch_q4k_repack(const void* src, int rows, int K, void* dst, cudaStream_t s);
+// GGUF Q6_K / Q8_0 rows -> the tiled layouts of qfmt.cuh (fmt 1 / 2).
+int launch_qfmt_repack(int fmt, const void* src, int rows, int K, void* dst, cudaStream_t s);
 int make_tmap_2d_16bit(CUtensorMap* map, const void* base, int rows, int cols, int row_stride,
                        int box_rows, int box_cols, int swizzle_bytes);
 

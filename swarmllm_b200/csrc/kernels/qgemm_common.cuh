@@ -64,6 +64,51 @@ SW_DEVICE void q4k_decode_scales(const uint4& hdr, float* s, float* mb) {
 #undef SB
 }
 
+// The 8 sub-block scales and mins as fp16 pairs, with packed integer ops:
+// S[i] = (d*sc_2i, d*sc_2i+1), NM[i] = (-dmin*m_2i, -dmin*m_2i+1).  Each 6-bit
+// value is placed under the 0x64 exponent byte (1024 + v), 1024 is subtracted
+// exactly and one HMUL2 applies d: the same single rounding as fp32 d*sc
+// converted to fp16.
+SW_DEVICE void q4k_scales_h2(const uint4& hdr, __half2 (&S)[4], __half2 (&NM)[4]) {
+  const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;
+  const uint32_t sc03 = w0 & 0x3F3F3F3Fu, m03 = w1 & 0x3F3F3F3Fu;
+  const uint32_t sc47 = and_or(w0 >> 2, 0x30303030u, w2 & 0x0F0F0F0Fu);
+  const uint32_t m47 = and_or(w1 >> 2, 0x30303030u, (w2 >> 4) & 0x0F0F0F0Fu);
+  const __half2 K1024 = u32_as_h2(0x64006400u);
+  const __half2 d2 = u32_as_h2((hdr.x & 0xFFFFu) * 0x10001u);
+  const __half2 nd2 = __hneg2(u32_as_h2((hdr.x >> 16) * 0x10001u));
+  const uint32_t sv[2] = {sc03, sc47}, mv[2] = {m03, m47};
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    S[2 * g] = __hmul2(__hsub2(u32_as_h2(__byte_perm(sv[g], 0x64646464u, 0x5140u)), K1024), d2);
+    S[2 * g + 1] =
+        __hmul2(__hsub2(u32_as_h2(__byte_perm(sv[g], 0x64646464u, 0x5342u)), K1024), d2);
+    NM[2 * g] = __hmul2(__hsub2(u32_as_h2(__byte_perm(mv[g], 0x64646464u, 0x5140u)), K1024), nd2);
+    NM[2 * g + 1] =
+        __hmul2(__hsub2(u32_as_h2(__byte_perm(mv[g], 0x64646464u, 0x5342u)), K1024), nd2);
+  }
+}
+
+// Sub-blocks [4h, 4h+4) of one row's superblock (K 128h .. 128h+127) into 64
+// TMEM columns at taddr + 64h, from the fp16 scale pairs of q4k_scales_h2.
+SW_DEVICE void dq_half_h2(const uint4 (&q)[8], const __half2 (&S)[4], const __half2 (&NM)[4],
+                          uint32_t taddr, int h) {
+  const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
+  const __half2 SIXTEENTH = u32_as_h2(0x2C002C00u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int sub = 4 * h + k;
+    const __half2 Sp = S[sub >> 1], Mp = NM[sub >> 1];
+    const __half2 Sj = (sub & 1) ? __high2half2(Sp) : __low2half2(Sp);
+    const __half2 MB = (sub & 1) ? __high2half2(Mp) : __low2half2(Mp);
+    const __half2 S16 = __hmul2(Sj, SIXTEENTH);
+    uint32_t cols[16];
+#pragma unroll
+    for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[4 * sub + w4], Sj, S16, MB, cols + 4 * w4);
+    tmem_st_x16(taddr + sub * 16, cols);
+  }
+}
+
 // Dequantize one row's superblock (256 K values) into the unit's 128 TMEM columns.
 SW_DEVICE void dq_unit(const uint4 (&q)[8], const float* sc, const float* mb, uint32_t taddr) {
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);

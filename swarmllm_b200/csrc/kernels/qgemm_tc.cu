@@ -1,6 +1,9 @@
-// Q4_K x fp16 GEMM on the 5th-generation tensor cores (tcgen05 / TMEM / TMA).
+// Quantized x fp16 GEMM on the 5th-generation tensor cores (tcgen05 / TMEM / TMA).
 //
-//   out[t][r] = sum_k W[r][k] * X[t][k],   W: Q4_K (repacked), X: fp16 [T, K]
+//   out[t][r] = sum_k W[r][k] * X[t][k],   W: Q4_K, Q6_K or Q8_0 (repacked), X: fp16 [T, K]
+//
+// The kernel is written once over a weight format (qfmt.cuh: repacked row
+// size, register dequantizer); the description below uses Q4_K.
 //
 // One kernel serves decode (T = 1..256 tokens, weight-streaming, bound by HBM)
 // and prefill (T up to thousands, tensor-bound).  It replaces the reference's
@@ -34,22 +37,22 @@
 #include "kernels.h"
 
 #include <cstdlib>
+#include <type_traits>
 #include "gemm_out.cuh"
-#include "qgemm_common.cuh"
+#include "qfmt.cuh"
 #include "tc_utils.cuh"
 #include "ep_common.cuh"
 
 namespace swarm {
 using namespace tc;
 
-constexpr int kWStageBytes = 128 * kQ4kRowBytes;  // 18432
 constexpr int kTmemCols = 512;
 
 // Per token-tile configuration.  Each dequantizer warpgroup owns its own pair
 // of TMEM A stages and its own W stages (the stage counts are multiples of the
 // warpgroup count), so a stage is always re-used by the warpgroup that used it
 // last and no parity wait can run two phases ahead.
-template <int N>
+template <class F, class FB, int N>
 struct QCfg {
   // Dequantizer warpgroups take units round-robin; each owns one "unit stage":
   // 128 TMEM columns of A (K=256 fp16) plus the unit's activation tile in smem,
@@ -67,17 +70,25 @@ struct QCfg {
   // NACC of them in flight.  The drain adds the accumulators.
   static constexpr int NACC = (A_COL / N) >= 4 ? 4 : ((A_COL / N) >= 2 ? 2 : 1);
   static constexpr int X_UNIT_BYTES = N * 512;           // N rows x 256 K fp16 (4 swizzle atoms)
-  static constexpr int W_ST = 2 * DQ;
+  // A stage holds one unit of either format (FB: the row tiles from split_tile on).
+  static constexpr int ROW_MAX = F::ROW_BYTES > FB::ROW_BYTES ? F::ROW_BYTES : FB::ROW_BYTES;
+  static constexpr int W_STAGE = 128 * ROW_MAX;          // 18 KB for Q4_K
   static_assert(A_COL >= NACC * N, "TMEM budget");
   static constexpr int X_BYTES = U * X_UNIT_BYTES;
-  static constexpr int W_BYTES = W_ST * kWStageBytes;
   static constexpr int BAR_BYTES = 512;
+  // Two W stages per warpgroup where they fit (one for the wider formats at
+  // the larger token tiles).
+  static constexpr int W_ST =
+      (1024 + X_BYTES + 2 * DQ * W_STAGE + BAR_BYTES <= 227 * 1024) ? 2 * DQ : DQ;
+  static constexpr int W_BYTES = W_ST * W_STAGE;
   static constexpr int SMEM = 1024 + X_BYTES + W_BYTES + BAR_BYTES;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
 struct QGemmArgs {
   const uint8_t* w;
+  const uint8_t* w_b;  // row tiles >= split_tile: second format's tensor (mixed-format GEMM)
+  int split_tile;
   int rows, K, T;
   int n_tok_tiles, ksb;
   long total_units;
@@ -111,10 +122,38 @@ struct QGemmArgs {
   } while (0)
 #endif
 
-template <int N>
-__global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
+// One dequantizer warp's part of a unit: stage -> registers (freeing the
+// stage), then each half of K (64 TMEM columns) once the MMAs that last read
+// that half of the unit's TMEM A stage have completed; each half is handed to
+// the MMA issuer on its own barrier, so the MMAs of the first half overlap the
+// dequantization of the second.
+template <class F>
+SW_DEVICE bool dq_unit_fmt(const uint8_t* stage, int row, uint64_t* w_empty, uint64_t* empty2,
+                           uint64_t* ready2, uint32_t empty_parity, uint32_t taddr, int* status,
+                           int i, int lane) {
+  typename F::Regs r;
+  F::load(reinterpret_cast<const uint4*>(stage + row * F::ROW_BYTES), r);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(w_empty);
+  F::prep(r);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (!mbar_wait_warp(&empty2[h], empty_parity, status, 32, i, h)) return false;
+    tc_fence_after();
+    F::dq_half(r, taddr, h);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ready2[h]);
+  }
+  return true;
+}
+
+template <class F, class FB, int N>
+__global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
     qgemm_q4k_tc_kernel(const __grid_constant__ CUtensorMap x_map, QGemmArgs a) {
-  using C = QCfg<N>;
+  using C = QCfg<F, FB, N>;
+  constexpr bool kMixed = !std::is_same<F, FB>::value;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -123,9 +162,10 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_smem + C::W_BYTES);
   uint64_t* w_full = bars;                 // W stage loaded (tx)
   uint64_t* w_empty = w_full + C::W_ST;    // W stage read by its warpgroup (4 warps)
-  uint64_t* ready = w_empty + C::W_ST;     // unit: A in TMEM (4 warps) + X in smem (producer + tx)
-  uint64_t* empty = ready + C::U;          // unit consumed by the MMAs (commit)
-  uint64_t* d_full = empty + C::U;
+  // Per unit stage s and K half h (index 2s + h):
+  uint64_t* ready = w_empty + C::W_ST;     // A half in TMEM (4 warps); h = 0 also X in smem (tx)
+  uint64_t* empty = ready + 2 * C::U;      // A half consumed by the MMAs (commit); h = 1 frees X
+  uint64_t* d_full = empty + 2 * C::U;
   uint64_t* d_empty = d_full + 1;
   uint64_t* done_bar = d_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
@@ -137,7 +177,12 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::W_ST; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
-    for (int i = 0; i < C::U; ++i) { mbar_init(&ready[i], 5); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < C::U; ++i) {
+      mbar_init(&ready[2 * i], 5);
+      mbar_init(&ready[2 * i + 1], 4);
+      mbar_init(&empty[2 * i], 1);
+      mbar_init(&empty[2 * i + 1], 1);
+    }
     mbar_init(d_full, 1);
     mbar_init(d_empty, 4);
     mbar_init(done_bar, 1);
@@ -164,9 +209,17 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
         const int wsi = i % C::W_ST;
         if (!(ok = mbar_wait(&w_empty[wsi], ((i / C::W_ST) & 1) ^ 1, a.status, 11, i, 0))) break;
         QTRACE(a.trace, i, 0);
-        mbar_arrive_expect_tx(&w_full[wsi], kWStageBytes);
-        bulk_load(w_smem + wsi * kWStageBytes,
-                  a.w + ((size_t)rt * a.ksb + sb) * kWStageBytes, kWStageBytes, &w_full[wsi]);
+        const uint8_t* wsrc;
+        int bytes;
+        if (kMixed && rt >= a.split_tile) {
+          bytes = 128 * FB::ROW_BYTES;
+          wsrc = a.w_b + ((size_t)(rt - a.split_tile) * a.ksb + sb) * bytes;
+        } else {
+          bytes = 128 * F::ROW_BYTES;
+          wsrc = a.w + ((size_t)rt * a.ksb + sb) * bytes;
+        }
+        mbar_arrive_expect_tx(&w_full[wsi], bytes);
+        bulk_load(w_smem + wsi * C::W_STAGE, wsrc, bytes, &w_full[wsi]);
         ++issued;
       }
       if (!ok)  // drain our own copies still in flight before the CTA exits
@@ -183,17 +236,18 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
       for (int i = 0; i < n_units && ok; ++i, (++sb == a.ksb) ? (sb = 0, ++tile) : 0) {
         const int nt = tile % a.n_tok_tiles;
         const int s = i % C::U;
-        if (!(ok = mbar_wait(&empty[s], ((i / C::U) & 1) ^ 1, a.status, 12, i, 0))) break;
-        mbar_arrive_expect_tx(&ready[s], C::X_UNIT_BYTES);
+        if (!(ok = mbar_wait(&empty[2 * s + 1], ((i / C::U) & 1) ^ 1, a.status, 12, i, 0))) break;
+        mbar_arrive_expect_tx(&ready[2 * s], C::X_UNIT_BYTES);
         uint8_t* dst = x_smem + s * C::X_UNIT_BYTES;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tma_load_2d(dst + c * (N * 128), &x_map, sb * 256 + c * 64, nt * N, &ready[s]);
+        for (int c = 0; c < 4; ++c)
+          tma_load_2d(dst + c * (N * 128), &x_map, sb * 256 + c * 64, nt * N, &ready[2 * s]);
         QTRACE(a.trace, i, 1);
         ++issued;
       }
       if (!ok)
         for (int i = max(0, issued - C::U); i < issued; ++i)
-          mbar_wait(&ready[i % C::U], (i / C::U) & 1, nullptr, 0);
+          mbar_wait(&ready[2 * (i % C::U)], (i / C::U) & 1, nullptr, 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -215,19 +269,24 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
           if (!(ok = mbar_wait(d_empty, (seg - 1) & 1, a.status, 21, i, seg))) break;
         }
         const int s = i % C::U;
-        if (!(ok = mbar_wait(&ready[s], (i / C::U) & 1, a.status, 22, i, 0))) break;
-        QTRACE(a.trace, i, 5);
-        tc_fence_after();
         const uint64_t xd = xdesc[0] + (uint64_t)((s * C::X_UNIT_BYTES) >> 4);
         const uint32_t ab = tmem_base + C::A_COL + s * 128;
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
-          const uint32_t acc = (uint32_t)((kk % C::NACC) * N);
-          umma_f16_ts(tmem_base + acc, ab + kk * 8,
-                      xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4), idesc,
-                      (first && kk < C::NACC) ? 0u : 1u);
+        for (int h = 0; h < 2; ++h) {
+          if (!(ok = mbar_wait(&ready[2 * s + h], (i / C::U) & 1, a.status, 22, i, h))) break;
+          if (h == 0) QTRACE(a.trace, i, 5);
+          tc_fence_after();
+#pragma unroll
+          for (int k8 = 0; k8 < 8; ++k8) {
+            const int kk = 8 * h + k8;
+            const uint32_t acc = (uint32_t)((kk % C::NACC) * N);
+            umma_f16_ts(tmem_base + acc, ab + kk * 8,
+                        xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4), idesc,
+                        (first && kk < C::NACC) ? 0u : 1u);
+          }
+          umma_commit(&empty[2 * s + h]);
         }
-        umma_commit(&empty[s]);
+        if (!ok) break;
         if (last) {
           umma_commit(d_full);
           ++seg;
@@ -254,25 +313,17 @@ __global__ void __launch_bounds__(QCfg<N>::THREADS, 1)
         const int wsi = i % C::W_ST;
         if (!(ok = mbar_wait_warp(&w_full[wsi], (i / C::W_ST) & 1, a.status, 31, i, 0))) break;
         if (lane == 0) QTRACE(tr, i, 2);
-        const uint4* src = reinterpret_cast<const uint4*>(w_smem + wsi * kWStageBytes +
-                                                           row * kQ4kRowBytes);
-        uint4 q[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) q[c] = src[c];
-        const uint4 hdr = src[8];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&w_empty[wsi]);
-        float sc_f[8], mb_f[8];
-        q4k_decode_scales(hdr, sc_f, mb_f);
         const int s = i % C::U;
-        if (!(ok = mbar_wait_warp(&empty[s], ((i / C::U) & 1) ^ 1, a.status, 32, i, 0))) break;
-        if (lane == 0) QTRACE(tr, i, 7);
-        tc_fence_after();
-        dq_unit(q, sc_f, mb_f, tmem_base + lane_off + C::A_COL + s * 128);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ready[s]);
+        const uint32_t taddr = tmem_base + lane_off + C::A_COL + s * 128;
+        const uint32_t par = ((i / C::U) & 1) ^ 1;
+        const uint8_t* stage = w_smem + wsi * C::W_STAGE;
+        if (kMixed && tile / a.n_tok_tiles >= a.split_tile)
+          ok = dq_unit_fmt<FB>(stage, row, &w_empty[wsi], &empty[2 * s], &ready[2 * s], par, taddr,
+                               a.status, i, lane);
+        else
+          ok = dq_unit_fmt<F>(stage, row, &w_empty[wsi], &empty[2 * s], &ready[2 * s], par, taddr,
+                              a.status, i, lane);
+        if (!ok) break;
         if (lane == 0) QTRACE(tr, i, 3);
       }
       if (last) {
@@ -366,6 +417,82 @@ __global__ void q4k_repack_kernel(const uint8_t* __restrict__ src, int rows, int
   for (int i = 0; i < 16; ++i) out[128 + i] = b[i];
 }
 
+// GGUF Q6_K [rows][K/256][210 B] -> [rows_pad/128][K/256][128][224 B] (qfmt.cuh).
+__global__ void q6k_repack_kernel(const uint8_t* __restrict__ src, int rows, int rows_pad, int K,
+                                  uint8_t* __restrict__ dst) {
+  const int ksb = K / 256;
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)rows_pad * ksb) return;
+  const int r = (int)(idx / ksb), sb = (int)(idx - (long)r * ksb);
+  uint32_t* out = reinterpret_cast<uint32_t*>(
+      dst + (((size_t)(r >> 7) * ksb + sb) * 128 + (r & 127)) * kQ6kRowBytes);
+  if (r >= rows) {
+    for (int i = 0; i < kQ6kRowBytes / 4; ++i) out[i] = 0;
+    return;
+  }
+  const uint8_t* b = src + ((size_t)r * ksb + sb) * 210;
+  const uint8_t* ql = b;
+  const uint8_t* qh = b + 128;
+  const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192);
+  const float d = __half2float(__ushort_as_half((uint16_t)(b[208] | (b[209] << 8))));
+  // 6-bit code of value k: the low nibble comes from ql, the top two bits from qh
+  // (each 128-value half: quarter q of the half uses ql bytes [64n + 32(q&1), +32),
+  // nibble q>>1, and qh bits 2q..2q+1 of byte 32n + l).
+  auto code = [&](int k) -> uint32_t {
+    const int n = k >> 7, rr = k & 127, qt = rr >> 5, l = rr & 31;
+    const uint8_t lb = ql[64 * n + 32 * (qt & 1) + l];
+    const uint32_t lo = (qt >> 1) ? (lb >> 4) : (lb & 0xF);
+    const uint32_t hi = (qh[32 * n + l] >> (2 * qt)) & 3;
+    return lo | (hi << 4);
+  };
+  for (int w = 0; w < 32; ++w) {   // low nibbles, nibble order 0,2,4,6,1,3,5,7
+    uint32_t word = 0;
+    for (int p = 0; p < 8; ++p) {
+      const int k = 8 * w + ((p < 4) ? 2 * p : 2 * (p - 4) + 1);
+      word |= (code(k) & 0xF) << (4 * p);
+    }
+    out[w] = word;
+  }
+  for (int s = 0; s < 16; ++s) {   // crumbs
+    uint32_t word = 0;
+    for (int e = 0; e < 2; ++e)
+      for (int j = 0; j < 4; ++j) {
+        const int k = 16 * s + 8 * e + 2 * j;
+        word |= (code(k) >> 4) << (8 * e + 2 * j);
+        word |= (code(k + 1) >> 4) << (16 + 8 * e + 2 * j);
+      }
+    out[32 + s] = word;
+  }
+  for (int s = 0; s < 16; s += 2) {   // fp16 d * sc, clamped to the fp16 range
+    const float a0 = fminf(fmaxf(d * (float)sc[s], -65504.f), 65504.f);
+    const float a1 = fminf(fmaxf(d * (float)sc[s + 1], -65504.f), 65504.f);
+    out[48 + s / 2] = (uint32_t)__half_as_ushort(__float2half_rn(a0)) |
+                      ((uint32_t)__half_as_ushort(__float2half_rn(a1)) << 16);
+  }
+}
+
+// GGUF Q8_0 [rows][K/32][34 B] -> [rows_pad/128][K/256][128][272 B] (qfmt.cuh):
+// codes as q ^ 0x80, then the superblock's 8 fp16 block scales.
+__global__ void q80_repack_kernel(const uint8_t* __restrict__ src, int rows, int rows_pad, int K,
+                                  uint8_t* __restrict__ dst) {
+  const int ksb = K / 256;
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)rows_pad * ksb) return;
+  const int r = (int)(idx / ksb), sb = (int)(idx - (long)r * ksb);
+  uint8_t* out = dst + (((size_t)(r >> 7) * ksb + sb) * 128 + (r & 127)) * kQ80RowBytes;
+  if (r >= rows) {
+    for (int i = 0; i < kQ80RowBytes; ++i) out[i] = 0;
+    return;
+  }
+  const uint8_t* b = src + ((size_t)r * (K / 32) + sb * 8) * 34;
+  for (int blk = 0; blk < 8; ++blk) {
+    const uint8_t* q = b + blk * 34;
+    for (int i = 0; i < 32; ++i) out[blk * 32 + i] = q[2 + i] ^ 0x80;
+    out[256 + 2 * blk] = q[0];
+    out[256 + 2 * blk + 1] = q[1];
+  }
+}
+
 }  // namespace swarm
 
 using namespace swarm;
@@ -434,21 +561,21 @@ static const int g_gemv_max_t = [] {
 }();
 int q4k_gemv_max_t() { return g_gemv_max_t; }
 
-int q4k_plan_max_ctas(int T, int num_sms) {
-  return T <= g_gemv_max_t ? q4k_gemv_ctas_per_sm(T) * num_sms : num_sms;
+int q4k_plan_max_ctas(int T, int num_sms, int fmt) {
+  return T <= g_gemv_max_t ? qgemv_ctas_per_sm(fmt, T) * num_sms : num_sms;
 }
 
 // Work decomposition shared by the launcher, the workspace sizing and GemmOut.
 // At <= q4k_gemv_max_t() tokens the units go to the GEMV's CTAs instead (same
 // partial-slot format, token tile 16).
 void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_tiles, int* ksb,
-                 long* total_units, int* upc, int* n_ctas, size_t* ws_floats) {
+                 long* total_units, int* upc, int* n_ctas, size_t* ws_floats, int fmt) {
   const int N = q4k_tc_tok_tile(T);
   const int ntt = (T + N - 1) / N;
   const int kb = K / 256;
   const int tiles = ((rows + 127) / 128) * ntt;
   const long total = (long)tiles * kb;
-  const int max_ctas = q4k_plan_max_ctas(T, num_sms);
+  const int max_ctas = q4k_plan_max_ctas(T, num_sms, fmt);
   const int u = (int)((total + max_ctas - 1) / max_ctas);
   const int ctas = (int)((total + u - 1) / u);
   *tok_tile = N;
@@ -460,15 +587,26 @@ void q4k_tc_plan(int rows, int K, int T, int num_sms, int* tok_tile, int* n_tok_
   *ws_floats = (size_t)(tiles + ctas) * N * 128;
 }
 
-template <int N>
+template <class F, class FB, int N>
 static int launch_n(const CUtensorMap& map, const QGemmArgs& a, int n_ctas, cudaStream_t s) {
-  using C = QCfg<N>;
+  using C = QCfg<F, FB, N>;
   static unsigned long long attr_done = 0;
-  if (!smem_attr_once(qgemm_q4k_tc_kernel<N>, C::SMEM, &attr_done)) return -3;
-  if (launch_pdl(qgemm_q4k_tc_kernel<N>, dim3(n_ctas), dim3(C::THREADS), C::SMEM, s, map, a) !=
-      cudaSuccess)
+  if (!smem_attr_once(qgemm_q4k_tc_kernel<F, FB, N>, C::SMEM, &attr_done)) return -3;
+  if (launch_pdl(qgemm_q4k_tc_kernel<F, FB, N>, dim3(n_ctas), dim3(C::THREADS), C::SMEM, s, map,
+                 a) != cudaSuccess)
     return -4;
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+template <class F, class FB = F>
+static int launch_f(int N, const CUtensorMap& map, const QGemmArgs& a, int n_ctas,
+                    cudaStream_t s) {
+  switch (N) {
+    case 16: return launch_n<F, FB, 16>(map, a, n_ctas, s);
+    case 32: return launch_n<F, FB, 32>(map, a, n_ctas, s);
+    case 64: return launch_n<F, FB, 64>(map, a, n_ctas, s);
+    default: return launch_n<F, FB, 128>(map, a, n_ctas, s);
+  }
 }
 
 
@@ -476,14 +614,20 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
                         int T, float* ws, size_t ws_floats_avail, int num_sms, int* status,
                         GemmOut* out, cudaStream_t s, const unsigned long long* peer_ws,
                         int n_peers, int* sig_ctl, const unsigned long long* sig_bases,
-                        long long sig_flag_off, int sig_rank, int owner_tiles) {
+                        long long sig_flag_off, int sig_rank, int owner_tiles, int fmt,
+                        const void* w_b, int fmt_b, int split_tile) {
   if (T <= 0) return 0;
-  if (K % 256 != 0 || rows % 128 != 0) return -1;
+  if (K % 256 != 0 || rows % 128 != 0 || fmt < 0 || fmt >= kNumQFmts) return -1;
+  const bool mixed = w_b != nullptr && fmt_b >= 0 && fmt_b != fmt;
+  if (mixed && !(fmt == kFmtQ4K && fmt_b == kFmtQ6K)) return -1;   // the Q4_K_M q|k|v mix
+  if (mixed && (split_tile <= 0 || split_tile >= rows / 128)) return -1;
+  // the GEMV's resident CTAs per SM follow the wider format's stages
+  const int plan_fmt = mixed && qfmt_row_bytes(fmt_b) > qfmt_row_bytes(fmt) ? fmt_b : fmt;
   if ((x_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return -5;
   int N, ntt, kb, upc, ctas;
   long total;
   size_t need;
-  q4k_tc_plan(rows, K, T, num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need);
+  q4k_tc_plan(rows, K, T, num_sms, &N, &ntt, &kb, &total, &upc, &ctas, &need, plan_fmt);
   if (need > ws_floats_avail) return -6;
   if (total >= (1L << 24)) return -8;   // GemmOut's segment lookup assumes fewer units
   if (out) {
@@ -501,10 +645,12 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
   if (T <= g_gemv_max_t)
     return launch_qgemv_q4k(w_packed, rows, K, x, x_stride, T, ws, kb, total, upc, ctas, status,
                             peer_ws, n_peers, sig_ctl, sig_bases, sig_flag_off, sig_rank, s,
-                            owner_tiles);
+                            owner_tiles, fmt, mixed ? w_b : nullptr, mixed ? fmt_b : -1,
+                            split_tile);
   CUtensorMap map;
   if (make_tmap_2d_16bit(&map, x, T, K, x_stride, N, 64, 128) != 0) return -2;
-  QGemmArgs a{(const uint8_t*)w_packed, rows, K, T, ntt, kb, total, upc, ws, status, g_trace};
+  QGemmArgs a{(const uint8_t*)w_packed, (const uint8_t*)w_b, mixed ? split_tile : 0, rows, K, T,
+              ntt, kb, total, upc, ws, status, g_trace};
   a.n_peers = 0;
   a.owner_tiles = 0;
   a.sig_ctl = nullptr;
@@ -521,11 +667,11 @@ int launch_qgemm_q4k_tc(const void* w_packed, int rows, int K, const __half* x, 
     a.owner_tiles = owner_tiles;
     if (owner_tiles > 0 && (rows / 128) > owner_tiles * n_peers) return -7;
   }
-  switch (N) {
-    case 16: return launch_n<16>(map, a, ctas, s);
-    case 32: return launch_n<32>(map, a, ctas, s);
-    case 64: return launch_n<64>(map, a, ctas, s);
-    default: return launch_n<128>(map, a, ctas, s);
+  if (mixed) return launch_f<FmtQ4K, FmtQ6K>(N, map, a, ctas, s);
+  switch (fmt) {
+    case kFmtQ4K: return launch_f<FmtQ4K>(N, map, a, ctas, s);
+    case kFmtQ6K: return launch_f<FmtQ6K>(N, map, a, ctas, s);
+    default: return launch_f<FmtQ80>(N, map, a, ctas, s);
   }
 }
 
@@ -534,5 +680,18 @@ int launch_q4k_repack(const void* src, int rows, int K, void* dst, cudaStream_t 
   const long n = (long)rows_pad * (K / 256);
   q4k_repack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)src, rows,
                                                                  rows_pad, K, (uint8_t*)dst);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_qfmt_repack(int fmt, const void* src, int rows, int K, void* dst, cudaStream_t s) {
+  if (fmt == kFmtQ4K) return launch_q4k_repack(src, rows, K, dst, s);
+  if ((fmt != kFmtQ6K && fmt != kFmtQ8_0) || K % 256 != 0) return -1;
+  const int rows_pad = (rows + 127) / 128 * 128;
+  const long n = (long)rows_pad * (K / 256);
+  const unsigned grid = (unsigned)((n + 127) / 128);
+  if (fmt == kFmtQ6K)
+    q6k_repack_kernel<<<grid, 128, 0, s>>>((const uint8_t*)src, rows, rows_pad, K, (uint8_t*)dst);
+  else
+    q80_repack_kernel<<<grid, 128, 0, s>>>((const uint8_t*)src, rows, rows_pad, K, (uint8_t*)dst);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -1;
 }

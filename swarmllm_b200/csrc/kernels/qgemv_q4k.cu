@@ -1,6 +1,7 @@
-// Q4_K x fp16 GEMV for decode at 1..2 tokens, on the CUDA cores.
+// Quantized x fp16 GEMV for decode at 1..2 tokens, on the CUDA cores.
 //
-//   out[t][r] = sum_k W[r][k] * X[t][k],   W: Q4_K (repacked, as qgemm_tc.cu), X: fp16 [T, K]
+//   out[t][r] = sum_k W[r][k] * X[t][k],   W: Q4_K / Q6_K / Q8_0 (repacked, as
+//   qgemm_tc.cu; the per-format row math is in qfmt.cuh), X: fp16 [T, K]
 //
 // At a handful of tokens the GEMM is a weight stream.  On the tensor cores a
 // 128 x N x 16 tcgen05.mma costs the same ~48 clocks for every N <= 64 and
@@ -15,7 +16,7 @@
 // same): a unit is (128-row tile, 256-K superblock); CTAs take contiguous
 // unit ranges; the partial of each tile segment goes to slot (tile + cta).
 // Inside a CTA, warp w owns rows [32w, 32w+32) of every unit: it streams its
-// 4.5 KB quarter of the unit (2 stages) and the unit's activations (T x 512 B,
+// quarter of the unit (32 repacked rows, 2 stages) and the unit's activations (T x 512 B,
 // 2 stages) into its own shared memory with bulk copies, so no warp ever
 // waits on another.  One lane = one weight row.
 //
@@ -29,10 +30,12 @@
 // 120 |x|max), so they stay finite for activations below ~500 in magnitude.
 #include "kernels.h"
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "ep_common.cuh"
 #include "gemm_out.cuh"
-#include "qgemm_common.cuh"
+#include "qfmt.cuh"
 #include "tc_utils.cuh"
 
 namespace swarm {
@@ -41,22 +44,27 @@ using namespace tc;
 constexpr int kGvWarps = 4;                          // one per 32-row quarter of a tile
 constexpr int kGvWStages = 2;                        // code stages per warp
 constexpr int kGvXStages = 2;                        // activation stages per warp
-constexpr int kGvQuarterBytes = 32 * kQ4kRowBytes;   // 4608
 // mbarriers of all warps, ahead of the stage buffers
 constexpr int kGvBarBytes = 256;
 static_assert(kGvWarps * (kGvWStages + kGvXStages) * 8 <= kGvBarBytes, "barrier area too small");
 
-template <int T>
+template <class F, class FB, int T>
 struct GvCfg {
+  static constexpr int ROW_MAX = F::ROW_BYTES > FB::ROW_BYTES ? F::ROW_BYTES : FB::ROW_BYTES;
+  static constexpr int QUARTER = 32 * ROW_MAX;              // one warp's rows of a unit
   static constexpr int X_STAGE = T * 512;                   // T x 256 fp16
-  static constexpr int WARP_BYTES = kGvWStages * kGvQuarterBytes + kGvXStages * X_STAGE;
+  static constexpr int WARP_BYTES = kGvWStages * QUARTER + kGvXStages * X_STAGE;
   static constexpr int SMEM = kGvBarBytes + kGvWarps * WARP_BYTES;
-  static_assert(WARP_BYTES % 16 == 0 && q4k_gemv_ctas_per_sm(T) * (SMEM + 1024) <= 228 * 1024,
+  static_assert(WARP_BYTES % 16 == 0 &&
+                    qgemv_ctas_per_sm(ROW_MAX == F::ROW_BYTES ? F::ID : FB::ID, T) *
+                            (SMEM + 1024) <= 228 * 1024,
                 "stage layout");
 };
 
 struct GemvArgs {
   const uint8_t* w;
+  const uint8_t* w_b;  // row tiles >= split_tile: second format's tensor (mixed-format GEMV)
+  int split_tile;
   const __half* x;
   int x_stride;   // elements
   int rows, K;
@@ -74,18 +82,34 @@ struct GemvArgs {
   int sig_rank;
 };
 
-SW_DEVICE __half2 u2h(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+// One unit of one warp: codes from the stage into registers (the stage is then
+// refilled), wait for the unit's activations, accumulate the dot products.
+template <class F, int T, class IssueW>
+SW_DEVICE bool gemv_unit(const uint8_t* stage, uint64_t* xb, const uint8_t* xstage, int i,
+                         float (&acc)[T], int w_next, int n, IssueW& issue_w, int* status,
+                         int warp, int lane) {
+  typename F::Regs r;
+  F::load(reinterpret_cast<const uint4*>(stage + lane * F::ROW_BYTES), r);
+  __syncwarp();
+  if (lane == 0 && w_next < n) issue_w();
+  F::gemv_prep(r);
+  if (!mbar_wait_warp(xb, (i / kGvXStages) & 1, status, 42, i, warp)) return false;
+  mbar_try_wait(smem_u32(xb), (i / kGvXStages) & 1);
+  F::template gemv<T>(r, reinterpret_cast<const uint4*>(xstage), acc, lane);
+  return true;
+}
 
-template <int T>
+template <class F, class FB, int T>
 __global__ void __launch_bounds__(kGvWarps * 32)
     qgemv_q4k_kernel(const __grid_constant__ GemvArgs a) {
-  using C = GvCfg<T>;
+  using C = GvCfg<F, FB, T>;
+  constexpr bool kMixed = !std::is_same<F, FB>::value;
   extern __shared__ __align__(128) uint8_t gv_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t* wfull = reinterpret_cast<uint64_t*>(gv_smem) + warp * (kGvWStages + kGvXStages);
   uint64_t* xfull = wfull + kGvWStages;
   uint8_t* wst = gv_smem + kGvBarBytes + warp * C::WARP_BYTES;
-  uint8_t* xst = wst + kGvWStages * kGvQuarterBytes;
+  uint8_t* xst = wst + kGvWStages * C::QUARTER;
 
   const long u0 = (long)blockIdx.x * a.upc;
   const long u1 = min(a.total_units, u0 + a.upc);
@@ -102,14 +126,27 @@ __global__ void __launch_bounds__(kGvWarps * 32)
   // activation stage once the unit's dot products are done.  Units are walked
   // with (tile, superblock) cursors: one division per CTA, none per unit.
   const int rt0 = (int)(u0 / a.ksb), sb0 = (int)(u0 - (long)rt0 * a.ksb);
-  const uint8_t* wsrc = a.w + (((size_t)rt0 * a.ksb + sb0) * 128 + warp * 32) * kQ4kRowBytes;
   int w_next = 0, x_next = 0, x_sb = sb0;   // lane 0's copy cursors
-  auto issue_w = [&]() {                    // codes of unit w_next (contiguous in the repack)
+  int w_rt = rt0, w_sb = sb0;
+  auto issue_w = [&]() {                    // this warp's 32 rows of unit w_next
     uint64_t* bar = &wfull[w_next % kGvWStages];
-    mbar_arrive_expect_tx(bar, kGvQuarterBytes);
-    bulk_load(wst + (w_next % kGvWStages) * kGvQuarterBytes,
-              wsrc + (size_t)w_next * (128 * kQ4kRowBytes), kGvQuarterBytes, bar);
+    const uint8_t* src;
+    int bytes;
+    if (kMixed && w_rt >= a.split_tile) {
+      bytes = 32 * FB::ROW_BYTES;
+      src = a.w_b + (((size_t)(w_rt - a.split_tile) * a.ksb + w_sb) * 128 + warp * 32) *
+                        FB::ROW_BYTES;
+    } else {
+      bytes = 32 * F::ROW_BYTES;
+      src = a.w + (((size_t)w_rt * a.ksb + w_sb) * 128 + warp * 32) * F::ROW_BYTES;
+    }
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_load(wst + (w_next % kGvWStages) * C::QUARTER, src, bytes, bar);
     ++w_next;
+    if (++w_sb == a.ksb) {
+      w_sb = 0;
+      ++w_rt;
+    }
   };
   auto issue_x = [&]() {
     uint64_t* bar = &xfull[x_next % kGvXStages];
@@ -127,10 +164,6 @@ __global__ void __launch_bounds__(kGvWarps * 32)
     while (x_next < min(n, kGvXStages)) issue_x();
   }
 
-  const uint32_t MAGIC = 0x64006400u;
-  const __half2 K1024 = u2h(0x64006400u);
-  const __half2 SIXTEENTH = u2h(0x2C002C00u);   // 1/16, 1/16
-  const __half2 M64 = u2h(0xD400D400u);         // -64, -64
   float acc[T];
 #pragma unroll
   for (int t = 0; t < T; ++t) acc[t] = 0.f;
@@ -141,75 +174,15 @@ __global__ void __launch_bounds__(kGvWarps * 32)
     uint64_t* wb = &wfull[i % kGvWStages];
     if (!(ok = mbar_wait_warp(wb, (i / kGvWStages) & 1, a.status, 41, i, warp))) break;
     mbar_try_wait(smem_u32(wb), (i / kGvWStages) & 1);   // every lane acquires the bytes
-    const uint4* src = reinterpret_cast<const uint4*>(wst + (i % kGvWStages) * kGvQuarterBytes +
-                                                       lane * kQ4kRowBytes);
-    uint4 q[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) q[c] = src[c];
-    const uint4 hdr = src[8];
-    __syncwarp();
-    if (lane == 0 && w_next < n) issue_w();
-    float sc[8], mb[8];
-    q4k_decode_scales(hdr, sc, mb);
+    const uint8_t* stage = wst + (i % kGvWStages) * C::QUARTER;
     uint64_t* xb = &xfull[i % kGvXStages];
-    if (!(ok = mbar_wait_warp(xb, (i / kGvXStages) & 1, a.status, 42, i, warp))) break;
-    mbar_try_wait(smem_u32(xb), (i / kGvXStages) & 1);
-    const uint4* xs = reinterpret_cast<const uint4*>(xst + (i % kGvXStages) * C::X_STAGE);
-
-    // sum_j m_j * (sum of x over sub-block j): lane l sums x[8l, 8l+8); four
-    // lanes make a sub-block; every lane then needs all eight sub-block sums.
-    float msum[T];
-#pragma unroll
-    for (int t = 0; t < T; ++t) {
-      const uint4 v = xs[t * 32 + lane];
-      const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(u2h(vw[e]));
-        s += f.x + f.y;
-      }
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      float m = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) m = fmaf(mb[j], __shfl_sync(0xffffffffu, s, 4 * j), m);
-      msum[t] = m;
-    }
-
-    const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      // four independent fp16 sums (one per nibble pair) keep the chains short
-      __half2 p0[T], p1[T], p2[T], p3[T];
-#pragma unroll
-      for (int t = 0; t < T; ++t) p0[t] = p1[t] = p2[t] = p3[t] = __float2half2_rn(0.f);
-#pragma unroll
-      for (int w4 = 0; w4 < 4; ++w4) {
-        const uint32_t xw = qw[4 * j + w4], hi = xw >> 8;
-        // (k0,k1), (k2,k3), (k4,k5), (k6,k7) as exact fp16 integers
-        const __half2 c0 = __hsub2(u2h(and_or(xw, 0x000F000Fu, MAGIC)), K1024);
-        const __half2 c1 = __hfma2(u2h(and_or(xw, 0x00F000F0u, MAGIC)), SIXTEENTH, M64);
-        const __half2 c2 = __hsub2(u2h(and_or(hi, 0x000F000Fu, MAGIC)), K1024);
-        const __half2 c3 = __hfma2(u2h(and_or(hi, 0x00F000F0u, MAGIC)), SIXTEENTH, M64);
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-          const uint4 xv = xs[t * 32 + 4 * j + w4];   // x[8w .. 8w+8) of this word
-          p0[t] = __hfma2(c0, u2h(xv.x), p0[t]);
-          p1[t] = __hfma2(c1, u2h(xv.y), p1[t]);
-          p2[t] = __hfma2(c2, u2h(xv.z), p2[t]);
-          p3[t] = __hfma2(c3, u2h(xv.w), p3[t]);
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < T; ++t) {
-        const float2 f0 = __half22float2(__hadd2(p0[t], p1[t]));
-        const float2 f1 = __half22float2(__hadd2(p2[t], p3[t]));
-        acc[t] = fmaf(sc[j], (f0.x + f0.y) + (f1.x + f1.y), acc[t]);
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < T; ++t) acc[t] -= msum[t];
+    if (kMixed && rt >= a.split_tile)
+      ok = gemv_unit<FB, T>(stage, xb, xst + (i % kGvXStages) * C::X_STAGE, i, acc, w_next, n,
+                            issue_w, a.status, warp, lane);
+    else
+      ok = gemv_unit<F, T>(stage, xb, xst + (i % kGvXStages) * C::X_STAGE, i, acc, w_next, n,
+                           issue_w, a.status, warp, lane);
+    if (!ok) break;
 
     __syncwarp();   // every lane is done with this activation stage
     if (lane == 0 && x_next < n) issue_x();
@@ -247,9 +220,9 @@ __global__ void __launch_bounds__(kGvWarps * 32)
     ep_grid_done_signal(a.sig_ctl, a.sig_bases, a.sig_flag_off, a.n_peers, a.sig_rank);
 }
 
-// The plan assumes q4k_gemv_ctas_per_sm(T) CTAs resident per SM (one wave);
+// The plan assumes qgemv_ctas_per_sm(fmt, T) CTAs resident per SM (one wave);
 // ask for the full shared-memory carveout so they fit.
-template <int T>
+template <class F, class FB, int T>
 static int setup_t() {
   // Function attributes apply to the current device: set them once per device.
   static unsigned long long done = 0;
@@ -257,42 +230,50 @@ static int setup_t() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
   const unsigned long long bit = 1ull << dev;
   if (__atomic_load_n(&done, __ATOMIC_ACQUIRE) & bit) return 1;
-  if (cudaFuncSetAttribute(qgemv_q4k_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           GvCfg<T>::SMEM) != cudaSuccess ||
-      cudaFuncSetAttribute(qgemv_q4k_kernel<T>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                           100) != cudaSuccess)
+  if (cudaFuncSetAttribute(qgemv_q4k_kernel<F, FB, T>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GvCfg<F, FB, T>::SMEM) != cudaSuccess ||
+      cudaFuncSetAttribute(qgemv_q4k_kernel<F, FB, T>,
+                           cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
     return -3;
   __atomic_fetch_or(&done, bit, __ATOMIC_RELEASE);
   return 1;
 }
 
-template <int T>
+template <class F, int T>
 static int occupancy_t() {
-  if (setup_t<T>() != 1) return -1;
+  if (setup_t<F, F, T>() != 1) return -1;
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qgemv_q4k_kernel<T>, kGvWarps * 32,
-                                                    GvCfg<T>::SMEM) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qgemv_q4k_kernel<F, F, T>, kGvWarps * 32,
+                                                    GvCfg<F, F, T>::SMEM) != cudaSuccess)
     return -1;
   return n;
 }
 
-template <int T>
+template <class F, class FB, int T>
 static int launch_t(const GemvArgs& a, int ctas, cudaStream_t s) {
-  if (setup_t<T>() != 1) return -3;
-  if (launch_pdl(qgemv_q4k_kernel<T>, dim3(ctas), dim3(kGvWarps * 32), GvCfg<T>::SMEM, s, a) !=
-      cudaSuccess)
+  if (setup_t<F, FB, T>() != 1) return -3;
+  if (launch_pdl(qgemv_q4k_kernel<F, FB, T>, dim3(ctas), dim3(kGvWarps * 32),
+                 GvCfg<F, FB, T>::SMEM, s, a) != cudaSuccess)
     return -4;
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+template <class F, class FB = F>
+static int launch_f(const GemvArgs& a, int T, int ctas, cudaStream_t s) {
+  return T == 1 ? launch_t<F, FB, 1>(a, ctas, s) : launch_t<F, FB, 2>(a, ctas, s);
 }
 
 }  // namespace swarm
 
 using namespace swarm;
 
-int q4k_gemv_occupancy(int T) {
-  switch (T) {
-    case 1: return occupancy_t<1>();
-    case 2: return occupancy_t<2>();
+int q4k_gemv_occupancy(int T, int fmt) {
+  if (T != 1 && T != 2) return 0;
+  switch (fmt) {
+    case kFmtQ4K: return T == 1 ? occupancy_t<FmtQ4K, 1>() : occupancy_t<FmtQ4K, 2>();
+    case kFmtQ6K: return T == 1 ? occupancy_t<FmtQ6K, 1>() : occupancy_t<FmtQ6K, 2>();
+    case kFmtQ8_0: return T == 1 ? occupancy_t<FmtQ80, 1>() : occupancy_t<FmtQ80, 2>();
     default: return 0;
   }
 }
@@ -301,13 +282,18 @@ int launch_qgemv_q4k(const void* w_packed, int rows, int K, const __half* x, int
                      float* ws, int ksb, long total_units, int upc, int ctas, int* status,
                      const unsigned long long* peer_ws, int n_peers, int* sig_ctl,
                      const unsigned long long* sig_bases, long long sig_flag_off, int sig_rank,
-                     cudaStream_t s, int owner_tiles) {
-  if (T < 1 || T > kQGemvMaxT) return -1;
+                     cudaStream_t s, int owner_tiles, int fmt, const void* w_b, int fmt_b,
+                     int split_tile) {
+  if (T < 1 || T > kQGemvMaxT || fmt < 0 || fmt >= kNumQFmts) return -1;
+  const bool mixed = w_b != nullptr && fmt_b >= 0 && fmt_b != fmt;
+  if (mixed && !(fmt == kFmtQ4K && fmt_b == kFmtQ6K)) return -1;
   if ((x_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0 ||
       (reinterpret_cast<uintptr_t>(w_packed) & 15) != 0)
     return -5;
   GemvArgs a{};
   a.w = static_cast<const uint8_t*>(w_packed);
+  a.w_b = mixed ? static_cast<const uint8_t*>(w_b) : nullptr;
+  a.split_tile = mixed ? split_tile : 0;
   a.x = x;
   a.x_stride = x_stride;
   a.rows = rows;
@@ -332,8 +318,10 @@ int launch_qgemv_q4k(const void* w_packed, int rows, int K, const __half* x, int
     a.owner_tiles = owner_tiles;
     if (owner_tiles > 0 && (rows / 128) > owner_tiles * n_peers) return -7;
   }
-  switch (T) {
-    case 1: return launch_t<1>(a, ctas, s);
-    default: return launch_t<2>(a, ctas, s);
+  if (mixed) return launch_f<FmtQ4K, FmtQ6K>(a, T, ctas, s);
+  switch (fmt) {
+    case kFmtQ4K: return launch_f<FmtQ4K>(a, T, ctas, s);
+    case kFmtQ6K: return launch_f<FmtQ6K>(a, T, ctas, s);
+    default: return launch_f<FmtQ80>(a, T, ctas, s);
   }
 }

@@ -325,3 +325,96 @@ def q4k_repack_host(blocks: np.ndarray, rows: int, K: int) -> np.ndarray:
     out[..., :128] = words.view(np.uint8).reshape(rows_pad, ksb, 128)
     out[..., 128:] = src[..., :16]
     return out.reshape(rows_pad // 128, 128, ksb, 144).transpose(0, 2, 1, 3).copy()
+
+
+def _q6k_codes(b: np.ndarray) -> np.ndarray:
+    """6-bit codes [..., 256] (unsigned, q + 32) of Q6_K blocks [..., 210]."""
+    ql, qh = b[..., 0:128].astype(np.uint32), b[..., 128:192].astype(np.uint32)
+    q = np.zeros(b.shape[:-1] + (256,), np.uint32)
+    for n in range(2):
+        l0, l1 = ql[..., 64 * n:64 * n + 32], ql[..., 64 * n + 32:64 * n + 64]
+        h = qh[..., 32 * n:32 * n + 32]
+        q[..., 128 * n:128 * n + 32] = (l0 & 0xF) | ((h & 3) << 4)
+        q[..., 128 * n + 32:128 * n + 64] = (l1 & 0xF) | (((h >> 2) & 3) << 4)
+        q[..., 128 * n + 64:128 * n + 96] = (l0 >> 4) | (((h >> 4) & 3) << 4)
+        q[..., 128 * n + 96:128 * n + 128] = (l1 >> 4) | (((h >> 6) & 3) << 4)
+    return q
+
+
+def _tile(out: np.ndarray, rows_pad: int, ksb: int, rb: int) -> np.ndarray:
+    return out.reshape(rows_pad // 128, 128, ksb, rb).transpose(0, 2, 1, 3).copy()
+
+
+def q6k_repack_host(blocks: np.ndarray, rows: int, K: int) -> np.ndarray:
+    """Host mirror of the device Q6_K repack (launch_qfmt_repack, format 1):
+    [rows_pad/128, K/256, 128, 224] = 32 low-nibble words (nibble order
+    0,2,4,6,1,3,5,7 per 8 values), 16 crumb words (sub-block s: the top bits
+    of K 16s+8e+2j at bit 8e+2j, of K+1 at bit 16+8e+2j) and 16 fp16 scales
+    d * sc."""
+    ksb = K // 256
+    rows_pad = (rows + 127) // 128 * 128
+    src = np.zeros((rows_pad, ksb, 210), np.uint8)
+    src[:rows] = blocks.reshape(rows, ksb, 210)
+    q = _q6k_codes(src)
+    perm = [0, 2, 4, 6, 1, 3, 5, 7]
+    v = (q & 0xF).reshape(rows_pad, ksb, 32, 8)
+    lo = np.zeros((rows_pad, ksb, 32), np.uint32)
+    for p in range(8):
+        lo |= v[..., perm[p]] << (4 * p)
+    hi = (q >> 4).reshape(rows_pad, ksb, 16, 2, 4, 2)      # s, e, j, (even, odd)
+    cr = np.zeros((rows_pad, ksb, 16), np.uint32)
+    for e in range(2):
+        for j in range(4):
+            cr |= hi[..., e, j, 0] << (8 * e + 2 * j)
+            cr |= hi[..., e, j, 1] << (16 + 8 * e + 2 * j)
+    d = _f16_from(src[..., 208:210])
+    sc = src[..., 192:208].view(np.int8).astype(np.float32)
+    scales = np.clip(d[..., None] * sc, -65504, 65504).astype(np.float16)
+    out = np.zeros((rows_pad, ksb, 224), np.uint8)
+    out[..., 0:128] = lo.view(np.uint8).reshape(rows_pad, ksb, 128)
+    out[..., 128:192] = cr.view(np.uint8).reshape(rows_pad, ksb, 64)
+    out[..., 192:224] = scales.view(np.uint8).reshape(rows_pad, ksb, 32)
+    return _tile(out, rows_pad, ksb, 224)
+
+
+def q80_repack_host(blocks: np.ndarray, rows: int, K: int) -> np.ndarray:
+    """Host mirror of the device Q8_0 repack (format 2): [rows_pad/128, K/256,
+    128, 272] = 256 codes q ^ 0x80 in K order, then 8 fp16 block scales."""
+    ksb = K // 256
+    rows_pad = (rows + 127) // 128 * 128
+    src = np.zeros((rows_pad, ksb, 8, 34), np.uint8)
+    src[:rows] = blocks.reshape(rows, ksb, 8, 34)
+    out = np.zeros((rows_pad, ksb, 272), np.uint8)
+    out[..., :256] = (src[..., 2:] ^ 0x80).reshape(rows_pad, ksb, 256)
+    out[..., 256:] = src[..., :2].reshape(rows_pad, ksb, 16)
+    out[rows:] = 0                                         # padding rows stay zero
+    return _tile(out, rows_pad, ksb, 272)
+
+
+def repacked_dequant_host(packed: np.ndarray, fmt: int, rows: int, K: int) -> np.ndarray:
+    """fp32 [rows, K] from a repacked tensor (format 1 = Q6_K, 2 = Q8_0),
+    decoded from the layout description alone, with the scale rounded to fp16
+    as the kernels do: the oracle of the repacked-format kernels."""
+    ksb = K // 256
+    rb = {1: 224, 2: 272}[fmt]
+    rows_pad = (rows + 127) // 128 * 128
+    t = packed.reshape(rows_pad // 128, ksb, 128, rb).transpose(0, 2, 1, 3).reshape(rows_pad, ksb, rb)
+    if fmt == 2:
+        q = (t[..., :256] ^ 0x80).view(np.int8).astype(np.float32).reshape(rows_pad, ksb, 8, 32)
+        d = t[..., 256:272].copy().view(np.float16).astype(np.float32)
+        w = q * d[..., None]
+    else:
+        lo = t[..., :128].copy().view(np.uint32)           # [.., 32]
+        cr = t[..., 128:192].copy().view(np.uint32)        # [.., 16]
+        sc = t[..., 192:224].copy().view(np.float16).astype(np.float32)
+        q = np.zeros((rows_pad, ksb, 256), np.int64)
+        perm = [0, 2, 4, 6, 1, 3, 5, 7]
+        for wi in range(32):
+            for p in range(8):
+                k = 8 * wi + perm[p]
+                s, e, j, odd = k // 16, (k % 16) // 8, (k % 8) // 2, k % 2
+                nib = (lo[..., wi] >> (4 * p)) & 0xF
+                top = (cr[..., s] >> (16 * odd + 8 * e + 2 * j)) & 3
+                q[..., k] = (nib | (top << 4)).astype(np.int64) - 32
+        w = q.reshape(rows_pad, ksb, 16, 16).astype(np.float32) * sc[..., None]
+    return w.reshape(rows_pad, K)[:rows]

@@ -97,6 +97,9 @@ class ModelConfig:
     embed_qtype: str = "F16"
     output_qtype: str = ""              # "" -> weight_qtype
     expert_qtype: str = ""              # "" -> weight_qtype
+    # per-tensor mix on top of weight_qtype: "q4_k_m" = Q6_K for the LM head and
+    # for attn_v / ffn_down of the layers more_bits_layer() picks
+    quant_mix: str = ""
 
     @property
     def q_dim(self) -> int:
@@ -124,6 +127,23 @@ class ModelConfig:
     @property
     def softmax_scale(self) -> float:
         return self.attn_scale or 1.0 / math.sqrt(self.head_dim)
+
+    def more_bits_layer(self, layer: int) -> bool:
+        """Layers a "k_m" mix stores at higher precision: the first and last
+        eighth of the stack and every third layer between them (the layers
+        whose quantization error costs the most perplexity)."""
+        n, e = self.n_layers, self.n_layers // 8
+        return layer < e or layer >= n - e or (layer - e) % 3 == 2
+
+    def tensor_qtype(self, name: str, layer: int = -1) -> str | None:
+        """Storage type the quant mix gives `name` (None: the default rule)."""
+        if self.quant_mix != "q4_k_m":
+            return None
+        if name == "output.weight":
+            return "Q6_K"
+        if name in ("attn_v.weight", "ffn_down.weight") and self.more_bits_layer(layer):
+            return "Q6_K"
+        return None
 
     def is_linear_attn(self, layer: int) -> bool:
         return bool(self.full_attn_interval) and (layer + 1) % self.full_attn_interval != 0
@@ -241,6 +261,14 @@ def llama33_70b() -> ModelConfig:
                        rms_eps=1e-5, weight_qtype="Q4_K", embed_qtype="F16", output_qtype="Q4_K")
 
 
+def llama33_70b_q4km() -> ModelConfig:
+    """Llama-3.3-70B with a Q4_K_M-like tensor mix: Q4_K weights, a Q6_K LM head,
+    Q6_K attn_v / ffn_down on the more_bits_layer() layers."""
+    cfg = llama33_70b()
+    cfg.name, cfg.quant_mix, cfg.output_qtype = "llama-3.3-70b-q4km", "q4_k_m", "Q6_K"
+    return cfg
+
+
 def gpt_oss_120b_style() -> ModelConfig:
     """gpt-oss-120B-style MoE (MXFP4 experts, bf16 attention; expert-parallel config)."""
     return ModelConfig(name="gpt-oss-120b-style", arch="gpt-oss", n_layers=36, hidden=2880,
@@ -272,6 +300,7 @@ PRESETS = {
     "llama-3.2-3b": llama32_3b,
     "llama-3.2-1b": llama32_1b,
     "llama-3.3-70b": llama33_70b,
+    "llama-3.3-70b-q4km": llama33_70b_q4km,
     "gpt-oss-120b-style": gpt_oss_120b_style,
     "qwen3-next-80b-a3b-style": qwen3_next_80b_style,
 }

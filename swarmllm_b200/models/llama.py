@@ -147,11 +147,9 @@ class LlamaGPU:
                         L.qkv_bias = torch.cat([bq[o + a:o + z] for o, (a, z) in zip(base, shares)])
                 else:
                     parts = [get(b + n) for n in ("attn_q.weight", "attn_k.weight", "attn_v.weight")]
-                    qt = parts[0][1]
-                    assert all(p[1] == qt for p in parts), "q/k/v must share a quant type"
-                    pieces = [split_rows(p[0], qt, p[2], a, z) if W > 1 else p[0]
+                    pieces = [(split_rows(p[0], p[1], p[2], a, z) if W > 1 else p[0], p[1], z - a)
                               for p, (a, z) in zip(parts, shares)]
-                    L.wqkv = QLinear(torch.cat(pieces), qt, rows, H, dev)
+                    L.wqkv = QLinear.from_parts(pieces, H, dev)
                     L.qkv_bias = None
                     if cfg.attn_bias:
                         L.qkv_bias = torch.cat([small(b + n)[a:z] for n, (a, z) in
@@ -188,7 +186,7 @@ class LlamaGPU:
                     up = split_rows(u[0], u[1], u[2], uoff + tr * F, uoff + (tr + 1) * F)
                 else:
                     gp, up = g[0], u[0]
-                L.wgu = QLinear(torch.cat([gp, up]), g[1], 2 * F, H, dev)
+                L.wgu = QLinear.from_parts([(gp, g[1], F), (up, u[1], F)], H, dev)
                 t, qt, shape = get(b + "ffn_down.weight")
                 if W > 1:
                     t = split_cols(t, qt, shape, tr * F, (tr + 1) * F)
@@ -588,7 +586,8 @@ class GpuForwardContext:
             self.moe = MoeWorkspace(dev, max_tokens, H, cfg.expert_ffn, cfg.n_experts,
                                     cfg.n_experts_used, ex.x_dtype, self.gemm.num_sms,
                                     ep=model.ep)
-            S = max(cfg.shared_expert_ffn, 1)
+            # this rank's shared-expert features (the whole expert, or its TP share)
+            S = max([L.sh_gu.rows // 2 for L in model.layers if L.sh_gu is not None] + [1])
             self.act_sh = torch.zeros(max_tokens, S, dtype=torch.float16, device=dev)
         # Size the CUDA-core GEMM scratch up front (graph capture cannot grow it).
         self.gemm.dense(max(max_tokens * model.max_gemm_rows(),

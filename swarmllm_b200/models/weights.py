@@ -99,6 +99,16 @@ def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
     specs.append(("output_norm.weight", (H,), Q.F32))
     if not cfg.tie_embeddings:
         specs.append(("output.weight", (cfg.vocab, H), oq))
+    if cfg.quant_mix:
+        mixed = []
+        for name, shape, qt in specs:
+            layer, base = -1, name
+            if name.startswith("blk."):
+                _, num, base = name.split(".", 2)
+                layer = int(num)
+            t = cfg.tensor_qtype(base, layer)
+            mixed.append((name, shape, Q.NAME_TO_TYPE[t] if t and len(shape) == 2 else qt))
+        specs = mixed
     return specs
 
 
@@ -168,7 +178,8 @@ class RandomSource:
         shape, qt = self.specs[name]
         n = int(np.prod(shape))
         dev_ok = device is not None and torch.device(device).type == "cuda"
-        if self.on_device and dev_ok and qt in (Q.Q4_K, Q.F16, Q.BF16, Q.MXFP4) and not _is_norm(name):
+        if self.on_device and dev_ok and qt in (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.F16, Q.BF16, Q.MXFP4) \
+                and not _is_norm(name):
             return _random_blocks_device(name, shape, qt, self.seed, self.std, device), qt, shape
         vals = _init_value(name, shape, self._rng(name), self.std)
         b = Q.quantize(vals.reshape(-1, shape[-1]), qt)
@@ -195,6 +206,26 @@ def _random_blocks_device(name, shape, qt, seed, std, device) -> torch.Tensor:
         e = int(round(np.log2(3 * std / 12.0))) + 128
         out[:, 0] = e
         out[:, 1:] = torch.randint(0, 256, (nb, 16), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+        return out.reshape(-1)
+    if qt == Q.Q6_K:
+        # codes q - 32 uniform in [-32, 31] (std 18.5); scales 30..63 (mean 46.5)
+        nb = n // 256
+        out = torch.empty(nb, 210, dtype=torch.uint8, device=device)
+        out[:, :192] = torch.randint(0, 256, (nb, 192), generator=g, device=device,
+                                     dtype=torch.int32).to(torch.uint8)
+        out[:, 192:208] = torch.randint(30, 64, (nb, 16), generator=g, device=device,
+                                        dtype=torch.int32).to(torch.uint8)
+        d = torch.full((nb,), std / (18.5 * 46.5), device=device, dtype=torch.float16)
+        out[:, 208:210] = d.view(torch.uint8).view(nb, 2)
+        return out.reshape(-1)
+    if qt == Q.Q8_0:
+        # int8 codes uniform in [-128, 127] (std 73.9)
+        nb = n // 32
+        out = torch.empty(nb, 34, dtype=torch.uint8, device=device)
+        d = torch.full((nb,), std / 73.9, device=device, dtype=torch.float16)
+        out[:, 0:2] = d.view(torch.uint8).view(nb, 2)
+        out[:, 2:] = torch.randint(0, 256, (nb, 32), generator=g, device=device,
+                                   dtype=torch.int32).to(torch.uint8)
         return out.reshape(-1)
     assert qt == Q.Q4_K
     nb = n // 256

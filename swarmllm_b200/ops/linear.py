@@ -3,8 +3,11 @@
 ``QLinear`` holds one (possibly row-concatenated) GGML-quantized weight
 ``[rows, K]`` and picks the kernel:
 
-* Q4_K with rows % 128 == 0 and K % 256 == 0: the tcgen05 tensor-core GEMM
-  (``qgemm_tc.cu``); the GGUF blocks are repacked on the device once at load.
+* Q4_K, Q6_K or Q8_0 with rows % 128 == 0 and K % 256 == 0: the tcgen05
+  tensor-core GEMM (``qgemm_tc.cu``; at 1..2 tokens the CUDA-core GEMV of
+  ``qgemv_q4k.cu``); the GGUF blocks are repacked on the device once at load
+  into the format's tiled layout (``qfmt.cuh``) and dequantized in registers.
+* F16 / BF16: the dense tcgen05 GEMM.
 * anything else: the CUDA-core kernel over the GGUF block layout
   (``qmatmul_simt.cu``), writing a dense fp32 result.
 
@@ -39,6 +42,8 @@ def stream_k_floats(max_tokens: int, rows: int, num_sms: int) -> int:
 DEQUANT_MIN_TOKENS = 64
 _DEQUANT_TYPES = (Q.Q4_0, Q.Q8_0, Q.Q4_K, Q.Q6_K, Q.IQ4_NL, Q.IQ4_XS, Q.MXFP4)
 _DQ_SCRATCH: dict = {}
+# GGML type -> repacked tensor-core format (qfmt.cuh) and its bytes per row per 256 K
+TC_FORMATS = {Q.Q4_K: (0, 144), Q.Q6_K: (1, 224), Q.Q8_0: (2, 272)}
 
 
 def _dequant_scratch(device, n: int) -> torch.Tensor:
@@ -103,10 +108,14 @@ class QLinear:
         self.w16 = None
         self.packed = None
         self.raw = raw
-        if not force_simt and qtype == Q.Q4_K and rows % 128 == 0 and K % 256 == 0:
+        self.fmt = -1
+        if not force_simt and qtype in TC_FORMATS and rows % 128 == 0 and K % 256 == 0:
+            # kind "q4k" names the repacked tensor-core path for every format
             self.kind = "q4k"
-            self.packed = torch.empty(rows * (K // 256) * 144, dtype=torch.uint8, device=self.device)
-            C().q4k_repack(raw, rows, K, self.packed)
+            self.fmt, row_bytes = TC_FORMATS[qtype]
+            self.packed = torch.empty(rows * (K // 256) * row_bytes, dtype=torch.uint8,
+                                      device=self.device)
+            C().qfmt_repack(self.fmt, raw, rows, K, self.packed)
             self.raw = None
         elif not force_simt and (qtype in (Q.F16, Q.BF16) or (qtype == Q.F32 and f32_as_f16)) \
                 and K % 8 == 0:
@@ -119,22 +128,57 @@ class QLinear:
                 self.kind = "dense"
                 self.w16 = src.to(torch.float16).contiguous()
                 self.raw = None
+        self.packed_b, self.fmt_b, self.split_tile = None, -1, 0
         self.use_tc = self.kind != "simt"
         self.bias = None
         if bias is not None:
             self.bias = torch.as_tensor(bias, dtype=torch.float32, device=self.device)
 
+    @classmethod
+    def from_parts(cls, parts, K: int, device) -> "QLinear":
+        """One GEMM over row-concatenated tensors [(data, qtype, rows), ...].
+        Parts of one type concatenate their bytes.  A leading Q4_K run and a
+        trailing Q6_K run (a Q4_K_M checkpoint's q|k|v: v is Q6_K in some
+        layers) become one mixed-format GEMM when the split falls on a 128-row
+        tile; any other mix is dequantized to one fp16 weight."""
+        types = [p[1] for p in parts]
+        rows = sum(int(p[2]) for p in parts)
+        dev = torch.device(device)
+        as_dev = [p[0] if isinstance(p[0], torch.Tensor) else
+                  torch.from_numpy(np.ascontiguousarray(p[0])) for p in parts]
+        as_dev = [t.reshape(-1).to(dev, dtype=torch.uint8) for t in as_dev]
+        if all(t == types[0] for t in types):
+            return cls(torch.cat(as_dev), types[0], rows, K, dev)
+        na = next(i for i, t in enumerate(types) if t != types[0])
+        rows_a = sum(int(p[2]) for p in parts[:na])
+        if (types[0] == Q.Q4_K and all(t == Q.Q6_K for t in types[na:]) and rows_a % 128 == 0
+                and rows % 128 == 0 and K % 256 == 0):
+            lin = cls(torch.cat(as_dev[:na]), Q.Q4_K, rows_a, K, dev)
+            lin_b = cls(torch.cat(as_dev[na:]), Q.Q6_K, rows - rows_a, K, dev)
+            lin.rows, lin.packed_b, lin.fmt_b = rows, lin_b.packed, lin_b.fmt
+            lin.split_tile = rows_a // 128
+            lin.qtype = -1      # mixed
+            return lin
+        w16 = torch.empty(rows, K, dtype=torch.float16, device=dev)
+        r0 = 0
+        for t, (_, qt, n) in zip(as_dev, parts):
+            C().dequant_f16(t, qt, int(n), K, w16[r0:r0 + int(n)])
+            r0 += int(n)
+        return cls(w16.view(torch.uint8).reshape(-1), Q.F16, rows, K, dev)
+
     @property
     def nbytes(self) -> int:
         t = {"q4k": self.packed, "dense": self.w16, "simt": self.raw}[self.kind]
-        return t.numel() * t.element_size()
+        extra = self.packed_b.numel() if self.packed_b is not None else 0
+        return t.numel() * t.element_size() + extra
 
     def __call__(self, x: torch.Tensor, ws: GemmWorkspace, out: torch.Tensor | None = None):
         """GEMM result of x [T, K] (fp16).  `out` (fp32 [T, rows]) gives the
         CUDA-core path its own output instead of the workspace's dense buffer."""
         T = x.shape[0]
         if self.kind == "q4k":
-            return C().qgemm_q4k_tc(self.packed, self.rows, self.K, x, ws.ws, ws.status, ws.num_sms)
+            return C().qgemm_q4k_tc(self.packed, self.rows, self.K, x, ws.ws, ws.status, ws.num_sms,
+                                    self.fmt, self.packed_b, self.fmt_b, self.split_tile)
         if self.kind == "dense":
             return C().dense_gemm_tc(self.w16, x, ws.ws, ws.status, ws.num_sms)
         if (T >= DEQUANT_MIN_TOKENS and self.qtype in _DEQUANT_TYPES and self.K % 8 == 0

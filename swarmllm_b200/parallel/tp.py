@@ -111,7 +111,7 @@ class TpGroup:
         owner_tiles = self.H // 128 // W
         return C().qgemm_q4k_tc_tp(lin.packed, lin.rows, lin.K, x, status, num_sms, own,
                                    self.ws_bytes // 4, dsts, self.ctl[4 * b:], self.bases,
-                                   self.flag_off + b * W * 4, r, owner_tiles)
+                                   self.flag_off + b * W * 4, r, owner_tiles, lin.fmt)
 
     def moe_partial(self, rows, wts, k: int, shared, shared_gate, T: int):
         """This rank's MoE output (its experts, its slice of the shared

@@ -2,7 +2,7 @@
 
     python -m swarmllm_b200.utils.kernel_cases \
         {qgemm|qgemm_sweep|qgemv|qgemv_o|dense|attn|attn_prefill|rmsnorm|swiglu|rope_kv|moe|delta|
-         delta_decode|tree_rank|sample} [--time]
+         delta_decode|tree_rank|sample} [--time] [--qtype Q4_K|Q6_K|Q8_0]
 
 Each case builds benchmark-sized operands on cuda:0 (inputs larger than the
 126 MB L2 where memory traffic matters; tree_rank and sample use the real
@@ -36,20 +36,22 @@ def _time(fn, n=50):
     ts.sort()
     print(f"{_CASE[0]}: median {ts[len(ts) // 2]:.1f} us over {n} calls")
 
-def rand_q4k(rows, K):
-    # random Q4_K blocks generated on the device (valid scales)
+def rand_q4k(rows, K, qt=Q.Q4_K):
+    # random GGML blocks generated on the device (valid scales)
     from swarmllm_b200.models.weights import _random_blocks_device
-    return _random_blocks_device("w", (rows, K), Q.Q4_K, 1, 0.02, dev)
+    return _random_blocks_device("w", (rows, K), qt, 1, 0.02, dev)
 
 
-def run_case(which: str, TIME: bool = False) -> None:
+def run_case(which: str, TIME: bool = False, qtype: str = "Q4_K") -> None:
     """Build one case's operands on cuda:0 and run its kernel a few times."""
     torch.manual_seed(0)
     _CASE[0] = which
     if which == "qgemm_sweep":  # the 70B projections at 1..2048 tokens: device time, GB/s, TFLOP/s
         from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+        qt = Q.NAME_TO_TYPE[qtype]
+        bv, bb = Q.BLOCK[qt]
         for rows, K, name in ((57344, 8192, "gate_up"), (8192, 28672, "down"), (8192, 8192, "o_proj")):
-            lin = QLinear(rand_q4k(rows, K), Q.Q4_K, rows, K, dev)
+            lin = QLinear(rand_q4k(rows, K, qt), qt, rows, K, dev)
             for T in (1, 3, 8, 16, 32, 64, 128, 2048):
                 ws = GemmWorkspace(dev, T, rows)
                 x = torch.randn(T, K, device=dev).half()
@@ -64,7 +66,8 @@ def run_case(which: str, TIME: bool = False) -> None:
                 b.record()
                 torch.cuda.synchronize()
                 us = a.elapsed_time(b) * 1000 / n
-                print(f"{name} {rows}x{K} T={T}: {us:8.1f} us  {rows * K * 0.5625 / us / 1e3:6.0f} GB/s"
+                print(f"{qtype} {name} {rows}x{K} T={T}: {us:8.1f} us  "
+                      f"{rows * K * bb / bv / us / 1e3:6.0f} GB/s"
                       f"  {2 * rows * K * T / us / 1e6:7.1f} TFLOP/s", flush=True)
                 ws.check()
     elif which == "qgemm":       # Llama-3.3-70B gate|up at decode batch 32 (264 MB of weights)
@@ -256,8 +259,9 @@ def run_case(which: str, TIME: bool = False) -> None:
 
 def main(argv=None) -> None:
     argv = sys.argv[1:] if argv is None else argv
-    which = next((a for a in argv if not a.startswith("--")), "qgemm")
-    run_case(which, "--time" in argv)
+    qtype = argv[argv.index("--qtype") + 1] if "--qtype" in argv else "Q4_K"
+    which = next((a for a in argv if not a.startswith("--") and a != qtype), "qgemm")
+    run_case(which, "--time" in argv, qtype)
 
 
 if __name__ == "__main__":

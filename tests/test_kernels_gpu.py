@@ -104,13 +104,49 @@ def test_prefill_dequant_dense_path(qt):
     wd = torch.from_numpy(Q.dequantize(b, qt).reshape(rows, K))
     x = _x(T, K, seed=5)
     ref = x.float() @ wd.T
-    lin = QLinear(b, qt, rows, K, DEV)
+    lin = QLinear(b, qt, rows, K, DEV, force_simt=True)   # not the repacked tensor-core path
     ws = GemmWorkspace(DEV, T, rows)
     g = lin(x.to(DEV), ws)
     out = _dense_from(g, T, rows)
     torch.cuda.synchronize()
     ws.check()
     assert rel_err(out.cpu(), ref) < 3e-3
+
+
+@pytest.mark.parametrize("qt,fmt", [(Q.Q6_K, 1), (Q.Q8_0, 2)])
+def test_qfmt_repack_matches_host(qt, fmt):
+    rows, K = 200, 768
+    rng = np.random.default_rng(4)
+    b = Q.quantize(rng.standard_normal((rows, K), dtype=np.float32) * 0.02, qt)
+    rb = C().qfmt_row_bytes(fmt)
+    dst = torch.full((256 * (K // 256) * rb,), 0xAB, dtype=torch.uint8, device=DEV)
+    C().qfmt_repack(fmt, torch.from_numpy(b).to(DEV), rows, K, dst)
+    host = (Q.q6k_repack_host if fmt == 1 else Q.q80_repack_host)(b, rows, K).reshape(-1)
+    assert np.array_equal(dst.cpu().numpy(), host)
+
+
+@pytest.mark.parametrize("qt,fmt", [(Q.Q6_K, 1), (Q.Q8_0, 2)])
+@pytest.mark.parametrize("rows,K,T,sms", [(384, 1024, 1, 0), (384, 1024, 2, 0), (1024, 4096, 7, 0),
+                                          (256, 8192, 33, 0), (640, 2048, 64, 0),
+                                          (384, 1024, 130, 0), (1280, 2048, 1, 9),
+                                          (1024, 2048, 40, 3), (512, 1024, 300, 4)])
+def test_qgemm_tc_formats(qt, fmt, rows, K, T, sms):
+    """Q6_K and Q8_0 on the repacked tensor-core GEMM (T > 2) and CUDA-core
+    GEMV (T <= 2), against the fp32 product with the repacked weights."""
+    from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
+    rng = np.random.default_rng(rows + K + T)
+    b = Q.quantize(rng.standard_normal((rows, K), dtype=np.float32) * 0.02, qt)
+    lin = QLinear(b, qt, rows, K, DEV)
+    assert lin.kind == "q4k" and lin.fmt == fmt
+    wd = torch.from_numpy(Q.repacked_dequant_host(
+        (Q.q6k_repack_host if fmt == 1 else Q.q80_repack_host)(b, rows, K).reshape(-1),
+        fmt, rows, K))
+    x = _x(T, K, seed=T + 2) * 2.0
+    ws = GemmWorkspace(DEV, T, rows, num_sms=sms or None)
+    out = _dense_from(lin(x.to(DEV), ws), T, rows)
+    torch.cuda.synchronize()
+    ws.check()
+    assert rel_err(out.cpu(), x.float() @ wd.T) < 3e-3
 
 
 def test_q4k_repack_matches_host():
