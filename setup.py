@@ -44,6 +44,10 @@ if os.environ.get("SWARMLLM_PTXAS_VERBOSE"):
 if os.environ.get("SWARMLLM_KERNEL_TRACE"):
     # Per-unit %globaltimer timelines of the GEMM / attention kernels (profiling only).
     NVCC_FLAGS += ["-DSWARMLLM_KERNEL_TRACE=1"]
+if os.environ.get("SWARMLLM_NVCC_DEFINES"):
+    # Extra -D flags selecting kernel variants (A/B experiments, e.g.
+    # -DSWARMLLM_QGEMM_HALVES=2).
+    NVCC_FLAGS += os.environ["SWARMLLM_NVCC_DEFINES"].split()
 if os.environ.get("SWARMLLM_DEVICE_CHECKS"):
     # Device-side bounds checks (record the bad index, skip the access).
     NVCC_FLAGS += ["-DSWARMLLM_DEVICE_CHECKS=1"]

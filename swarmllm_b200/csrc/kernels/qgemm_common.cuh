@@ -64,6 +64,25 @@ SW_DEVICE void q4k_decode_scales(const uint4& hdr, float* s, float* mb) {
 #undef SB
 }
 
+// fp32 d * sc_j and dmin * m_j from the 16-byte header, with packed byte
+// masks and the 2^23 float trick for the byte -> float conversions (exact).
+SW_DEVICE void q4k_scales_f32(const uint4& hdr, float* s, float* mb) {
+  const float d = half_bits_to_f((uint16_t)(hdr.x & 0xFFFF));
+  const float dmin = half_bits_to_f((uint16_t)(hdr.x >> 16));
+  const uint32_t w0 = hdr.y, w1 = hdr.z, w2 = hdr.w;
+  const uint32_t sv[2] = {w0 & 0x3F3F3F3Fu, and_or(w0 >> 2, 0x30303030u, w2 & 0x0F0F0F0Fu)};
+  const uint32_t mv[2] = {w1 & 0x3F3F3F3Fu, and_or(w1 >> 2, 0x30303030u, (w2 >> 4) & 0x0F0F0F0Fu)};
+  const float M23 = 8388608.f;   // float bits 0x4B0000bb = 2^23 + bb
+#pragma unroll
+  for (int g = 0; g < 2; ++g)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      s[4 * g + b] = d * (__int_as_float((int)__byte_perm(sv[g], 0x4B000000u, 0x7650u + b)) - M23);
+      mb[4 * g + b] =
+          dmin * (__int_as_float((int)__byte_perm(mv[g], 0x4B000000u, 0x7650u + b)) - M23);
+    }
+}
+
 // The 8 sub-block scales and mins as fp16 pairs, with packed integer ops:
 // S[i] = (d*sc_2i, d*sc_2i+1), NM[i] = (-dmin*m_2i, -dmin*m_2i+1).  Each 6-bit
 // value is placed under the 0x64 exponent byte (1024 + v), 1024 is subtracted

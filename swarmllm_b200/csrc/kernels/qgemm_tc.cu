@@ -23,7 +23,8 @@
 //    straight into TMEM and the MMA reads its A operand from TMEM
 //    (tcgen05.mma ... [a_tmem]); shared memory only carries the raw 4.5-bit
 //    codes and the activations, so it is not the bottleneck at decode.
-//  * Activations arrive by TMA (128 B swizzle, K-major canonical layout); the
+//  * Activations arrive by TMA (128 B swizzle, K-major canonical layout) into
+//    their own ring of up to 8 unit tiles, loaded well ahead of the MMAs; the
 //    fp32 accumulator lives in TMEM columns [0, N).
 //  * Persistent, stream-K balanced: the (row_tile, token_tile, superblock)
 //    units are split evenly over the CTAs; each CTA writes one fp32 partial
@@ -48,19 +49,22 @@ using namespace tc;
 
 constexpr int kTmemCols = 512;
 
-// Per token-tile configuration.  Each dequantizer warpgroup owns its own pair
-// of TMEM A stages and its own W stages (the stage counts are multiples of the
-// warpgroup count), so a stage is always re-used by the warpgroup that used it
-// last and no parity wait can run two phases ahead.
+// Per token-tile configuration.
 template <class F, class FB, int N>
 struct QCfg {
-  // Dequantizer warpgroups take units round-robin; each owns one "unit stage":
-  // 128 TMEM columns of A (K=256 fp16) plus the unit's activation tile in smem,
-  // released by one MMA commit.  Stage counts are multiples of DQ, so every
-  // stage is re-used by the warpgroup that used it last and no parity wait can
-  // run two phases ahead.
+  // Dequantizer warpgroups take units round-robin; each owns one "unit stage"
+  // of 128 TMEM columns (A for K = 256 fp16), released by MMA commits.  The W
+  // stage counts are multiples of DQ, so every W stage is re-used by the
+  // warpgroup that used it last and no parity wait can run two phases ahead.
   static constexpr int DQ = N <= 64 ? 3 : 2;
   static constexpr int U = DQ;                           // unit stages in flight
+  // Hand-offs per unit between the dequantizers and the MMA issuer: 2 = per
+  // K half (64 columns), so the first half's MMAs overlap the second half's
+  // dequantization; 1 = whole units (fewer barrier round trips).
+#ifndef SWARMLLM_QGEMM_HALVES
+#define SWARMLLM_QGEMM_HALVES 1
+#endif
+  static constexpr int HALVES = SWARMLLM_QGEMM_HALVES;
   static constexpr int THREADS = 96 + 128 * DQ;          // W producer, MMA, X producer, DQ WGs
   static constexpr int FIRST_DQ_WARP = 3;
   static constexpr int A_COL = kTmemCols - 128 * U;      // accumulators use [0, NACC * N)
@@ -74,15 +78,23 @@ struct QCfg {
   static constexpr int ROW_MAX = F::ROW_BYTES > FB::ROW_BYTES ? F::ROW_BYTES : FB::ROW_BYTES;
   static constexpr int W_STAGE = 128 * ROW_MAX;          // 18 KB for Q4_K
   static_assert(A_COL >= NACC * N, "TMEM budget");
-  static constexpr int X_BYTES = U * X_UNIT_BYTES;
   static constexpr int BAR_BYTES = 512;
-  // Two W stages per warpgroup where they fit (one for the wider formats at
-  // the larger token tiles).
+  // The activation tiles have their own ring, X_ST units deep, independent
+  // of the TMEM stages: their TMA loads (L2 hits, but with the latency of an
+  // SM whose HBM queue is full) run that many units ahead of the MMAs.
+  // Two W stages per warpgroup unless that costs X stages below 4.
+  static constexpr int x_room(int w_st) {
+    return (227 * 1024 - 1024 - BAR_BYTES - w_st * W_STAGE) / X_UNIT_BYTES;
+  }
   static constexpr int W_ST =
-      (1024 + X_BYTES + 2 * DQ * W_STAGE + BAR_BYTES <= 227 * 1024) ? 2 * DQ : DQ;
+      x_room(2 * DQ) >= (x_room(DQ) < 4 ? x_room(DQ) : 4) ? 2 * DQ : DQ;
+  static constexpr int X_ST = x_room(W_ST) < 8 ? x_room(W_ST) : 8;
+  static_assert(X_ST >= 2, "activation ring");
+  static constexpr int X_BYTES = X_ST * X_UNIT_BYTES;
   static constexpr int W_BYTES = W_ST * W_STAGE;
   static constexpr int SMEM = 1024 + X_BYTES + W_BYTES + BAR_BYTES;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert((2 * W_ST + 2 * U * HALVES + 2 * X_ST + 3) * 8 + 4 <= BAR_BYTES, "barriers");
 };
 
 struct QGemmArgs {
@@ -123,13 +135,11 @@ struct QGemmArgs {
 #endif
 
 // One dequantizer warp's part of a unit: stage -> registers (freeing the
-// stage), then each half of K (64 TMEM columns) once the MMAs that last read
-// that half of the unit's TMEM A stage have completed; each half is handed to
-// the MMA issuer on its own barrier, so the MMAs of the first half overlap the
-// dequantization of the second.
-template <class F>
-SW_DEVICE bool dq_unit_fmt(const uint8_t* stage, int row, uint64_t* w_empty, uint64_t* empty2,
-                           uint64_t* ready2, uint32_t empty_parity, uint32_t taddr, int* status,
+// stage), then the unit's TMEM A stage in H hand-offs (H = 2: one per K half
+// of 64 columns), each once the MMAs that last read that part have completed.
+template <class F, int H>
+SW_DEVICE bool dq_unit_fmt(const uint8_t* stage, int row, uint64_t* w_empty, uint64_t* empty_h,
+                           uint64_t* ready_h, uint32_t empty_parity, uint32_t taddr, int* status,
                            int i, int lane) {
   typename F::Regs r;
   F::load(reinterpret_cast<const uint4*>(stage + row * F::ROW_BYTES), r);
@@ -137,14 +147,15 @@ SW_DEVICE bool dq_unit_fmt(const uint8_t* stage, int row, uint64_t* w_empty, uin
   if (lane == 0) mbar_arrive(w_empty);
   F::prep(r);
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    if (!mbar_wait_warp(&empty2[h], empty_parity, status, 32, i, h)) return false;
+  for (int h = 0; h < H; ++h) {
+    if (!mbar_wait_warp(&empty_h[h], empty_parity, status, 32, i, h)) return false;
     tc_fence_after();
-    F::dq_half(r, taddr, h);
+#pragma unroll
+    for (int q = 0; q < 2 / H; ++q) F::dq_half(r, taddr, h * (2 / H) + q);
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&ready2[h]);
+    if (lane == 0) mbar_arrive(&ready_h[h]);
   }
   return true;
 }
@@ -162,10 +173,12 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(w_smem + C::W_BYTES);
   uint64_t* w_full = bars;                 // W stage loaded (tx)
   uint64_t* w_empty = w_full + C::W_ST;    // W stage read by its warpgroup (4 warps)
-  // Per unit stage s and K half h (index 2s + h):
-  uint64_t* ready = w_empty + C::W_ST;     // A half in TMEM (4 warps); h = 0 also X in smem (tx)
-  uint64_t* empty = ready + 2 * C::U;      // A half consumed by the MMAs (commit); h = 1 frees X
-  uint64_t* d_full = empty + 2 * C::U;
+  // Per unit stage s and hand-off h (index s * HALVES + h):
+  uint64_t* ready = w_empty + C::W_ST;     // A part in TMEM (4 warps)
+  uint64_t* empty = ready + C::HALVES * C::U;   // A part consumed by the MMAs (commit)
+  uint64_t* x_full = empty + C::HALVES * C::U;  // activation stage loaded (tx)
+  uint64_t* x_empty = x_full + C::X_ST;         // activation stage consumed (commit)
+  uint64_t* d_full = x_empty + C::X_ST;
   uint64_t* d_empty = d_full + 1;
   uint64_t* done_bar = d_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
@@ -177,11 +190,13 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::W_ST; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }
-    for (int i = 0; i < C::U; ++i) {
-      mbar_init(&ready[2 * i], 5);
-      mbar_init(&ready[2 * i + 1], 4);
-      mbar_init(&empty[2 * i], 1);
-      mbar_init(&empty[2 * i + 1], 1);
+    for (int i = 0; i < C::U * C::HALVES; ++i) {
+      mbar_init(&ready[i], 4);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < C::X_ST; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
     }
     mbar_init(d_full, 1);
     mbar_init(d_empty, 4);
@@ -235,19 +250,19 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
       int tile = (int)(u0 / a.ksb), sb = (int)(u0 - (long)tile * a.ksb);
       for (int i = 0; i < n_units && ok; ++i, (++sb == a.ksb) ? (sb = 0, ++tile) : 0) {
         const int nt = tile % a.n_tok_tiles;
-        const int s = i % C::U;
-        if (!(ok = mbar_wait(&empty[2 * s + 1], ((i / C::U) & 1) ^ 1, a.status, 12, i, 0))) break;
-        mbar_arrive_expect_tx(&ready[2 * s], C::X_UNIT_BYTES);
-        uint8_t* dst = x_smem + s * C::X_UNIT_BYTES;
+        const int xs = i % C::X_ST;
+        if (!(ok = mbar_wait(&x_empty[xs], ((i / C::X_ST) & 1) ^ 1, a.status, 12, i, 0))) break;
+        mbar_arrive_expect_tx(&x_full[xs], C::X_UNIT_BYTES);
+        uint8_t* dst = x_smem + xs * C::X_UNIT_BYTES;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-          tma_load_2d(dst + c * (N * 128), &x_map, sb * 256 + c * 64, nt * N, &ready[2 * s]);
+          tma_load_2d(dst + c * (N * 128), &x_map, sb * 256 + c * 64, nt * N, &x_full[xs]);
         QTRACE(a.trace, i, 1);
         ++issued;
       }
       if (!ok)
-        for (int i = max(0, issued - C::U); i < issued; ++i)
-          mbar_wait(&ready[2 * (i % C::U)], (i / C::U) & 1, nullptr, 0);
+        for (int i = max(0, issued - C::X_ST); i < issued; ++i)
+          mbar_wait(&x_full[i % C::X_ST], (i / C::X_ST) & 1, nullptr, 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -255,10 +270,7 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
       const uint32_t idesc = idesc_f16(128, N, /*f16*/ 0);
       // Descriptor of each X stage; per-MMA K offsets are compile-time adds to
       // the start-address field (16-byte units).
-      uint64_t xdesc[C::U];
-#pragma unroll
-      for (int st = 0; st < C::U; ++st)
-        xdesc[st] = smem_desc(smem_u32(x_smem + st * C::X_UNIT_BYTES), 16, 1024, 2);
+      const uint64_t xdesc0 = smem_desc(smem_u32(x_smem), 16, 1024, 2);
       int seg = 0;
       bool ok = true;
       int sb = (int)(u0 % a.ksb);
@@ -269,24 +281,29 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
           if (!(ok = mbar_wait(d_empty, (seg - 1) & 1, a.status, 21, i, seg))) break;
         }
         const int s = i % C::U;
-        const uint64_t xd = xdesc[0] + (uint64_t)((s * C::X_UNIT_BYTES) >> 4);
+        const int xs = i % C::X_ST;
+        if (!(ok = mbar_wait(&x_full[xs], (i / C::X_ST) & 1, a.status, 23, i, 0))) break;
+        const uint64_t xd = xdesc0 + (uint64_t)((xs * C::X_UNIT_BYTES) >> 4);
         const uint32_t ab = tmem_base + C::A_COL + s * 128;
+        constexpr int KPH = 16 / C::HALVES;   // MMAs per hand-off
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (!(ok = mbar_wait(&ready[2 * s + h], (i / C::U) & 1, a.status, 22, i, h))) break;
+        for (int h = 0; h < C::HALVES; ++h) {
+          if (!(ok = mbar_wait(&ready[s * C::HALVES + h], (i / C::U) & 1, a.status, 22, i, h)))
+            break;
           if (h == 0) QTRACE(a.trace, i, 5);
           tc_fence_after();
 #pragma unroll
-          for (int k8 = 0; k8 < 8; ++k8) {
-            const int kk = 8 * h + k8;
+          for (int k8 = 0; k8 < KPH; ++k8) {
+            const int kk = KPH * h + k8;
             const uint32_t acc = (uint32_t)((kk % C::NACC) * N);
             umma_f16_ts(tmem_base + acc, ab + kk * 8,
                         xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4), idesc,
                         (first && kk < C::NACC) ? 0u : 1u);
           }
-          umma_commit(&empty[2 * s + h]);
+          umma_commit(&empty[s * C::HALVES + h]);
         }
         if (!ok) break;
+        umma_commit(&x_empty[xs]);
         if (last) {
           umma_commit(d_full);
           ++seg;
@@ -317,12 +334,13 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
         const uint32_t taddr = tmem_base + lane_off + C::A_COL + s * 128;
         const uint32_t par = ((i / C::U) & 1) ^ 1;
         const uint8_t* stage = w_smem + wsi * C::W_STAGE;
+        constexpr int H = C::HALVES;
         if (kMixed && tile / a.n_tok_tiles >= a.split_tile)
-          ok = dq_unit_fmt<FB>(stage, row, &w_empty[wsi], &empty[2 * s], &ready[2 * s], par, taddr,
-                               a.status, i, lane);
+          ok = dq_unit_fmt<FB, H>(stage, row, &w_empty[wsi], &empty[s * H], &ready[s * H], par,
+                                  taddr, a.status, i, lane);
         else
-          ok = dq_unit_fmt<F>(stage, row, &w_empty[wsi], &empty[2 * s], &ready[2 * s], par, taddr,
-                              a.status, i, lane);
+          ok = dq_unit_fmt<F, H>(stage, row, &w_empty[wsi], &empty[s * H], &ready[s * H], par,
+                                 taddr, a.status, i, lane);
         if (!ok) break;
         if (lane == 0) QTRACE(tr, i, 3);
       }

@@ -6,10 +6,9 @@
 // At a handful of tokens the GEMM is a weight stream.  On the tensor cores a
 // 128 x N x 16 tcgen05.mma costs the same ~48 clocks for every N <= 64 and
 // the hand-offs around it stretch that further, so the swap-AB kernel tops
-// out near a third of HBM bandwidth there; this kernel instead spends about
-// 13 issue slots per 8 weights per warp lane and keeps HBM the limit.
-// (Reference: the mmvq dp4a path for <= 8 rows, candle quantized/cuda.rs:291;
-// activations stay fp16 here instead of being quantized to int8.)
+// out near a third of HBM bandwidth there; this kernel works on the CUDA
+// cores instead.  (Reference: the mmvq dp4a path for <= 8 rows, candle
+// quantized/cuda.rs:291.)
 //
 // Layout and decomposition (shared with the tensor-core kernel, so the
 // stream-K partial format read by every epilogue -- gemm_out.cuh -- is the
@@ -20,16 +19,19 @@
 // 2 stages) into its own shared memory with bulk copies, so no warp ever
 // waits on another.  One lane = one weight row.
 //
-// Per 32-bit word of codes (8 weights, nibble order 0,2,4,6,1,3,5,7 from the
-// repack): LOP3 builds fp16 pairs 1024+q (low nibbles) or 1024+16q (high
-// nibbles); an HSUB2, resp. an HFMA2 by (1/16, -64), turns them into the exact
-// integers q; HFMA2 multiplies by the activation pair.  The sub-block scale
-// and min are applied once per 32 weights in fp32:
-//   sum_k (sc*q_k - m) x_k = sc * sum_k q_k x_k - m * sum_k x_k.
-// The fp16 partial sums hold 4 products each and are added in pairs (|sum| <=
-// 120 |x|max), so they stay finite for activations below ~500 in magnitude.
+// Q4_K (the common case) runs on integer dot products: each warp quantizes
+// the unit's activations to int8 (one scale per 32 values, as llama.cpp's
+// q8_1 activations for its mmvq kernels), then per 32-bit word of codes (8
+// weights) two masks split the nibbles into int8x4 words and two dp4a
+// accumulate them; the sub-block scale and min are applied once per 32
+// weights in fp32 (qfmt.cuh FmtQ4K::gemv_i8).  That is about 5 issue slots
+// per 8 weights instead of 13 for fp16 dequantization, so the weight stream
+// is no longer issue-bound; the activation rounding adds ~0.5 % relative
+// error.  SWARMLLM_GEMV_I8=0 selects the fp16 path (FmtQ4K::gemv), which the
+// other formats always take.
 #include "kernels.h"
 
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -48,12 +50,13 @@ constexpr int kGvXStages = 2;                        // activation stages per wa
 constexpr int kGvBarBytes = 256;
 static_assert(kGvWarps * (kGvWStages + kGvXStages) * 8 <= kGvBarBytes, "barrier area too small");
 
-template <class F, class FB, int T>
+template <class F, class FB, int T, bool I8 = false>
 struct GvCfg {
   static constexpr int ROW_MAX = F::ROW_BYTES > FB::ROW_BYTES ? F::ROW_BYTES : FB::ROW_BYTES;
   static constexpr int QUARTER = 32 * ROW_MAX;              // one warp's rows of a unit
   static constexpr int X_STAGE = T * 512;                   // T x 256 fp16
-  static constexpr int WARP_BYTES = kGvWStages * QUARTER + kGvXStages * X_STAGE;
+  static constexpr int XQ_BYTES = I8 ? T * (256 + 64) : 0;  // int8 x + (dx, sum) per 32
+  static constexpr int WARP_BYTES = kGvWStages * QUARTER + kGvXStages * X_STAGE + XQ_BYTES;
   static constexpr int SMEM = kGvBarBytes + kGvWarps * WARP_BYTES;
   static_assert(WARP_BYTES % 16 == 0 &&
                     qgemv_ctas_per_sm(ROW_MAX == F::ROW_BYTES ? F::ID : FB::ID, T) *
@@ -84,9 +87,9 @@ struct GemvArgs {
 
 // One unit of one warp: codes from the stage into registers (the stage is then
 // refilled), wait for the unit's activations, accumulate the dot products.
-template <class F, int T, class IssueW>
-SW_DEVICE bool gemv_unit(const uint8_t* stage, uint64_t* xb, const uint8_t* xstage, int i,
-                         float (&acc)[T], int w_next, int n, IssueW& issue_w, int* status,
+template <class F, int T, bool I8, class IssueW>
+SW_DEVICE bool gemv_unit(const uint8_t* stage, uint64_t* xb, const uint8_t* xstage, uint8_t* xq,
+                         int i, float (&acc)[T], int w_next, int n, IssueW& issue_w, int* status,
                          int warp, int lane) {
   typename F::Regs r;
   F::load(reinterpret_cast<const uint4*>(stage + lane * F::ROW_BYTES), r);
@@ -95,14 +98,22 @@ SW_DEVICE bool gemv_unit(const uint8_t* stage, uint64_t* xb, const uint8_t* xsta
   F::gemv_prep(r);
   if (!mbar_wait_warp(xb, (i / kGvXStages) & 1, status, 42, i, warp)) return false;
   mbar_try_wait(smem_u32(xb), (i / kGvXStages) & 1);
-  F::template gemv<T>(r, reinterpret_cast<const uint4*>(xstage), acc, lane);
+  if constexpr (I8) {
+    uint2* xq8 = reinterpret_cast<uint2*>(xq);
+    float2* xs2 = reinterpret_cast<float2*>(xq + T * 256);
+    quantize_x8<T>(reinterpret_cast<const uint4*>(xstage), xq8, xs2, lane);
+    __syncwarp();
+    F::template gemv_i8<T>(r, xq8, xs2, acc);
+  } else {
+    F::template gemv<T>(r, reinterpret_cast<const uint4*>(xstage), acc, lane);
+  }
   return true;
 }
 
-template <class F, class FB, int T>
+template <class F, class FB, int T, bool I8>
 __global__ void __launch_bounds__(kGvWarps * 32)
     qgemv_q4k_kernel(const __grid_constant__ GemvArgs a) {
-  using C = GvCfg<F, FB, T>;
+  using C = GvCfg<F, FB, T, I8>;
   constexpr bool kMixed = !std::is_same<F, FB>::value;
   extern __shared__ __align__(128) uint8_t gv_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -110,6 +121,7 @@ __global__ void __launch_bounds__(kGvWarps * 32)
   uint64_t* xfull = wfull + kGvWStages;
   uint8_t* wst = gv_smem + kGvBarBytes + warp * C::WARP_BYTES;
   uint8_t* xst = wst + kGvWStages * C::QUARTER;
+  uint8_t* xq = xst + kGvXStages * C::X_STAGE;   // int8 activations (I8 only)
 
   const long u0 = (long)blockIdx.x * a.upc;
   const long u1 = min(a.total_units, u0 + a.upc);
@@ -177,10 +189,12 @@ __global__ void __launch_bounds__(kGvWarps * 32)
     const uint8_t* stage = wst + (i % kGvWStages) * C::QUARTER;
     uint64_t* xb = &xfull[i % kGvXStages];
     if (kMixed && rt >= a.split_tile)
-      ok = gemv_unit<FB, T>(stage, xb, xst + (i % kGvXStages) * C::X_STAGE, i, acc, w_next, n,
+      ok = gemv_unit<FB, T, false>(stage, xb, xst + (i % kGvXStages) * C::X_STAGE, xq, i, acc,
+                                   w_next, n,
                             issue_w, a.status, warp, lane);
     else
-      ok = gemv_unit<F, T>(stage, xb, xst + (i % kGvXStages) * C::X_STAGE, i, acc, w_next, n,
+      ok = gemv_unit<F, T, I8>(stage, xb, xst + (i % kGvXStages) * C::X_STAGE, xq, i, acc,
+                               w_next, n,
                            issue_w, a.status, warp, lane);
     if (!ok) break;
 
@@ -222,7 +236,7 @@ __global__ void __launch_bounds__(kGvWarps * 32)
 
 // The plan assumes qgemv_ctas_per_sm(fmt, T) CTAs resident per SM (one wave);
 // ask for the full shared-memory carveout so they fit.
-template <class F, class FB, int T>
+template <class F, class FB, int T, bool I8>
 static int setup_t() {
   // Function attributes apply to the current device: set them once per device.
   static unsigned long long done = 0;
@@ -230,10 +244,10 @@ static int setup_t() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
   const unsigned long long bit = 1ull << dev;
   if (__atomic_load_n(&done, __ATOMIC_ACQUIRE) & bit) return 1;
-  if (cudaFuncSetAttribute(qgemv_q4k_kernel<F, FB, T>,
+  if (cudaFuncSetAttribute(qgemv_q4k_kernel<F, FB, T, I8>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           GvCfg<F, FB, T>::SMEM) != cudaSuccess ||
-      cudaFuncSetAttribute(qgemv_q4k_kernel<F, FB, T>,
+                           GvCfg<F, FB, T, I8>::SMEM) != cudaSuccess ||
+      cudaFuncSetAttribute(qgemv_q4k_kernel<F, FB, T, I8>,
                            cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
     return -3;
   __atomic_fetch_or(&done, bit, __ATOMIC_RELEASE);
@@ -242,26 +256,38 @@ static int setup_t() {
 
 template <class F, int T>
 static int occupancy_t() {
-  if (setup_t<F, F, T>() != 1) return -1;
+  constexpr bool I8 = F::ID == kFmtQ4K;
+  if (setup_t<F, F, T, I8>() != 1) return -1;
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qgemv_q4k_kernel<F, F, T>, kGvWarps * 32,
-                                                    GvCfg<F, F, T>::SMEM) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qgemv_q4k_kernel<F, F, T, I8>,
+                                                    kGvWarps * 32,
+                                                    GvCfg<F, F, T, I8>::SMEM) != cudaSuccess)
     return -1;
   return n;
 }
 
-template <class F, class FB, int T>
+template <class F, class FB, int T, bool I8>
 static int launch_t(const GemvArgs& a, int ctas, cudaStream_t s) {
-  if (setup_t<F, FB, T>() != 1) return -3;
-  if (launch_pdl(qgemv_q4k_kernel<F, FB, T>, dim3(ctas), dim3(kGvWarps * 32),
-                 GvCfg<F, FB, T>::SMEM, s, a) != cudaSuccess)
+  if (setup_t<F, FB, T, I8>() != 1) return -3;
+  if (launch_pdl(qgemv_q4k_kernel<F, FB, T, I8>, dim3(ctas), dim3(kGvWarps * 32),
+                 GvCfg<F, FB, T, I8>::SMEM, s, a) != cudaSuccess)
     return -4;
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
+// Q4_K (unmixed) takes the integer-dot variant unless SWARMLLM_GEMV_I8=0.
+static const bool g_gemv_i8 = [] {
+  const char* v = getenv("SWARMLLM_GEMV_I8");
+  return v ? atoi(v) != 0 : true;
+}();
+
 template <class F, class FB = F>
 static int launch_f(const GemvArgs& a, int T, int ctas, cudaStream_t s) {
-  return T == 1 ? launch_t<F, FB, 1>(a, ctas, s) : launch_t<F, FB, 2>(a, ctas, s);
+  if constexpr (F::ID == kFmtQ4K && std::is_same<F, FB>::value) {
+    if (g_gemv_i8)
+      return T == 1 ? launch_t<F, FB, 1, true>(a, ctas, s) : launch_t<F, FB, 2, true>(a, ctas, s);
+  }
+  return T == 1 ? launch_t<F, FB, 1, false>(a, ctas, s) : launch_t<F, FB, 2, false>(a, ctas, s);
 }
 
 }  // namespace swarm

@@ -17,6 +17,15 @@ def C():
     return _C()
 
 
+# Q4_K at 1..2 tokens runs the CUDA-core GEMV on int8 activations (one scale
+# per 32 values): ~0.5 % relative error from the activation rounding.
+GEMV_I8_TOL = 1.2e-2
+
+
+def q4k_tol(T):
+    return GEMV_I8_TOL if T <= 2 else 3e-3
+
+
 def rel_err(a, b):
     a, b = a.double(), b.double()
     return float((a - b).norm() / (b.norm() + 1e-30))
@@ -67,7 +76,7 @@ def test_qgemm_q4k_tc(rows, K, T):
     torch.cuda.synchronize()
     ws.check()
     e = rel_err(out.cpu(), ref)
-    assert e < 3e-3, e
+    assert e < q4k_tol(T), e
 
 
 @pytest.mark.parametrize("rows,K", [(384, 1024), (1280, 8192)])
@@ -89,7 +98,7 @@ def test_qgemv_q4k_strided(rows, K, T):
     out = _dense_from(lin(big.to(DEV)[:, 8:K + 8], ws), T, rows)
     torch.cuda.synchronize()
     ws.check()
-    assert rel_err(out.cpu(), ref) < 3e-3
+    assert rel_err(out.cpu(), ref) < q4k_tol(T)
 
 
 @pytest.mark.parametrize("qt", [Q.Q4_0, Q.Q8_0, Q.Q6_K, Q.IQ4_NL, Q.IQ4_XS, Q.MXFP4])
@@ -178,7 +187,7 @@ def test_qgemm_tc_multi_unit_ctas(rows, K, T, sms):
     out = _dense_from(g, T, rows)
     torch.cuda.synchronize()
     ws.check()
-    assert rel_err(out.cpu(), x.float() @ wd.T) < 3e-3
+    assert rel_err(out.cpu(), x.float() @ wd.T) < q4k_tol(T)
 
 
 def test_qgemm_tc_stream_k_many_segments():
@@ -511,7 +520,7 @@ def test_swiglu_on_stream_k_partials(T, kind):
     C().epi_swiglu(lin(x.to(DEV), ws), None, F, kind, False, 1.702, 7.0, out)
     torch.cuda.synchronize()
     ws.check()
-    assert rel_err(out.float().cpu(), ref) < 4e-3
+    assert rel_err(out.float().cpu(), ref) < (1.5e-2 if T <= 2 else 4e-3)
 
 
 @pytest.mark.parametrize("with_bias", [False, True])

@@ -95,8 +95,10 @@ def test_noalloc_matches_regular_entry_point_twice(rows, K, Ts):
         torch.cuda.synchronize()
         assert torch.isfinite(out).all()
         assert _rel_err(out.cpu(), ref.cpu()) < 3e-3, (call, T)
-        # and against the dequantized fp32 product
-        assert _rel_err(out.cpu(), x.cpu().float() @ wd.T) < 3e-3, (call, T)
+        # and against the dequantized fp32 product (1..2 tokens: the GEMV's
+        # int8 activations add ~0.5 % relative error)
+        tol = 1.2e-2 if T <= 2 else 3e-3
+        assert _rel_err(out.cpu(), x.cpu().float() @ wd.T) < tol, (call, T)
 
 
 def test_noalloc_rejects_oversized_problem():
