@@ -66,7 +66,7 @@ struct FmtQ4K {
   // Integer-dot variant of gemv (decode at 1..2 tokens): the activations of
   // the unit are quantized to int8 per 32 values (xq, built by quantize_x8
   // below), so 8 weights cost two nibble masks and two dp4a:
-  //   sum_k (sc q_k - m) x_k ~= sc dx sum_k q_k xq_k - m sum_k x_k.
+  //   sum_k (sc q_k - m) x_k ~= sc dx sum_k q_k xq_k - m dx sum_k xq_k.
   // The repacked nibble order puts K offsets (0,4,1,5) in the low nibbles
   // of a word's bytes and (2,6,3,7) in the high ones; quantize_x8 stores
   // the int8 activations in that order.
@@ -92,7 +92,7 @@ struct FmtQ4K {
       }
 #pragma unroll
       for (int t = 0; t < T; ++t) {
-        const float2 dsum = xs2[t * 8 + j];   // (dx, sum of x) of sub-block j
+        const float2 dsum = xs2[t * 8 + j];   // (dx, sum of the rounded x) of sub-block j
         acc[t] = fmaf(r.sc[j] * dsum.x, (float)is[t], acc[t]);
         acc[t] = fmaf(-r.mb[j], dsum.y, acc[t]);
       }
@@ -168,8 +168,11 @@ struct FmtQ4K {
 // The activations of one 256-K unit as int8 for FmtQ4K::gemv_i8, built by the
 // 32 lanes of a warp from the fp16 stage (lane l owns x[8l, 8l+8)): per 32
 // values one scale dx = max|x| / 127 (round to nearest through the 1.5 * 2^23
-// float trick), the int8 words in the repacked nibble order, and the fp32 sum
-// of the 32 fp16 values (for the min term).  xq: [T][32] uint2, xs2: [T][8].
+// float trick), the int8 words in the repacked nibble order, and dx times the
+// sum of the 32 rounded values.  The min term uses that sum of the rounded
+// activations, so the result is exactly W . x_rounded: the rounding error is
+// not multiplied by the (all-positive) scaled codes alone.
+// xq: [T][32] uint2, xs2: [T][8] (dx, dx * sum).
 template <int T>
 SW_DEVICE void quantize_x8(const uint4* xs, uint2* xq, float2* xs2, int lane) {
 #pragma unroll
@@ -180,19 +183,24 @@ SW_DEVICE void quantize_x8(const uint4* xs, uint2* xq, float2* xs2, int lane) {
     // values k = 0..7 of this lane's word: (f0.x, f0.y, f1.x, f1.y, f2.x, f2.y, f3.x, f3.y)
     float amax = fmaxf(fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y))),
                        fmaxf(fmaxf(fabsf(f2.x), fabsf(f2.y)), fmaxf(fabsf(f3.x), fabsf(f3.y))));
-    float sum = ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     const float inv = amax > 0.f ? 127.f / amax : 0.f;
     const float M = 12582912.f;   // 1.5 * 2^23: the low mantissa byte is round(v) mod 256
-    auto q8 = [&](float x) { return (uint32_t)__float_as_int(fmaf(x, inv, M)) & 0xFFu; };
+    float sum = 0.f;
+    auto q8 = [&](float x) {
+      const float r = fmaf(x, inv, M);
+      sum += r - M;               // the rounded value, exactly
+      return (uint32_t)__float_as_int(r) & 0xFFu;
+    };
     // low-nibble partners: K (0, 4, 1, 5); high-nibble partners: K (2, 6, 3, 7)
     const uint32_t lo = q8(f0.x) | (q8(f2.x) << 8) | (q8(f0.y) << 16) | (q8(f2.y) << 24);
     const uint32_t hi = q8(f1.x) | (q8(f3.x) << 8) | (q8(f1.y) << 16) | (q8(f3.y) << 24);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     xq[t * 32 + lane] = make_uint2(lo, hi);
-    if ((lane & 3) == 0) xs2[t * 8 + (lane >> 2)] = make_float2(amax * (1.f / 127.f), sum);
+    const float dx = amax * (1.f / 127.f);
+    if ((lane & 3) == 0) xs2[t * 8 + (lane >> 2)] = make_float2(dx, dx * sum);
   }
 }
 

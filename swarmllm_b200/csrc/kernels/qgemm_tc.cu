@@ -61,6 +61,11 @@ struct QCfg {
   // Hand-offs per unit between the dequantizers and the MMA issuer: 2 = per
   // K half (64 columns), so the first half's MMAs overlap the second half's
   // dequantization; 1 = whole units (fewer barrier round trips).
+// Timing experiments only (results are wrong): 1 = dequantizers skip the
+// TMEM writes, 2 = the MMA issuer skips the MMAs (commits still flow).
+#ifndef SWARMLLM_QGEMM_EXPERIMENT
+#define SWARMLLM_QGEMM_EXPERIMENT 0
+#endif
 #ifndef SWARMLLM_QGEMM_HALVES
 #define SWARMLLM_QGEMM_HALVES 1
 #endif
@@ -150,8 +155,10 @@ SW_DEVICE bool dq_unit_fmt(const uint8_t* stage, int row, uint64_t* w_empty, uin
   for (int h = 0; h < H; ++h) {
     if (!mbar_wait_warp(&empty_h[h], empty_parity, status, 32, i, h)) return false;
     tc_fence_after();
+#if SWARMLLM_QGEMM_EXPERIMENT != 1
 #pragma unroll
     for (int q = 0; q < 2 / H; ++q) F::dq_half(r, taddr, h * (2 / H) + q);
+#endif
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
@@ -296,6 +303,7 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
           for (int k8 = 0; k8 < KPH; ++k8) {
             const int kk = KPH * h + k8;
             const uint32_t acc = (uint32_t)((kk % C::NACC) * N);
+            if (SWARMLLM_QGEMM_EXPERIMENT != 2)
             umma_f16_ts(tmem_base + acc, ab + kk * 8,
                         xd + (uint64_t)((((kk >> 2) * (N * 128)) + (kk & 3) * 32) >> 4), idesc,
                         (first && kk < C::NACC) ? 0u : 1u);

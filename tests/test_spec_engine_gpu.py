@@ -24,10 +24,16 @@ def _ecfg(**kw):
 
 
 def _plain(cfg, prompts, params):
+    """The plain engine's tokens.  One or two decoding sequences run on the
+    CUDA-core GEMV with int8 activations, while speculative verify steps (many
+    rows) run the fp16 tensor-core GEMM; random-init models have near-tied
+    logits everywhere, so the reference decodes at least three sequences (the
+    extra ones are discarded) to stay on the same GEMM path."""
     from swarmllm_b200.engine import LLMEngine
     from swarmllm_b200.models.weights import RandomSource
     eng = LLMEngine.from_config(cfg, DEV, _ecfg(), source=RandomSource(cfg, seed=7))
-    return [o.token_ids for o in eng.generate(prompts, params)]
+    pad = [list(range(1, 9))] * max(0, 3 - len(prompts))
+    return [o.token_ids for o in eng.generate(prompts + pad, params)][:len(prompts)]
 
 
 def _spec(cfg, prompts, params, draft):
