@@ -103,7 +103,8 @@ void moe_localize(Tensor ids, Tensor wts, Tensor counts, int64_t E, int64_t e0, 
 GemmResult moe_combine_tp(Tensor rows, Tensor wts, int64_t k, const GemmResult* sh,
                           const GemmResult* shg, int64_t T, int64_t H, int64_t recv_base,
                           int64_t src_stride, std::vector<int64_t> dst_ptrs, Tensor sig_ctl,
-                          std::vector<int64_t> sig_bases, int64_t sig_flag_off, int64_t rank) {
+                          std::vector<int64_t> sig_bases, int64_t sig_flag_off, int64_t rank,
+                          bool to_all) {
   CHECK_DT(rows, at::kFloat); CHECK_DT(wts, at::kFloat); CHECK_DT(sig_ctl, at::kInt);
   TORCH_CHECK(!dst_ptrs.empty() && dst_ptrs.size() <= 8 && dst_ptrs.size() == sig_bases.size(),
               "1..8 ranks");
@@ -117,7 +118,7 @@ GemmResult moe_combine_tp(Tensor rows, Tensor wts, int64_t k, const GemmResult* 
   int rc = launch_moe_combine_tp(rows.data_ptr<float>(), (int)rows.stride(0), wts.data_ptr<float>(),
                                  (int)k, sh ? &sh->g : nullptr, shg ? &shg->g : nullptr, (int)T,
                                  (int)H, W, d, sig_ctl.data_ptr<int>(), b,
-                                 (long long)sig_flag_off, (int)rank, cur_stream());
+                                 (long long)sig_flag_off, (int)rank, cur_stream(), to_all ? 1 : 0);
   TORCH_CHECK(rc == 0, "moe_combine_tp failed: rc=", rc);
   GemmResult r;
   r.g = swarm::GemmOut{};
@@ -159,7 +160,7 @@ void register_moe_ops(py::module& m) {
   m.def("moe_combine_tp", &moe_combine_tp, py::arg("rows"), py::arg("wts"), py::arg("k"),
         py::arg("sh").none(true), py::arg("shg").none(true), py::arg("T"), py::arg("H"),
         py::arg("recv_base"), py::arg("src_stride"), py::arg("dst_ptrs"), py::arg("sig_ctl"),
-        py::arg("sig_bases"), py::arg("sig_flag_off"), py::arg("rank"));
+        py::arg("sig_bases"), py::arg("sig_flag_off"), py::arg("rank"), py::arg("to_all") = false);
   m.def("mxfp4_repack", &mxfp4_repack);
   m.def("moe_packed_bytes", &moe_packed_bytes);
   m.def("moe_tok_tile", &moe_tok_tile);

@@ -205,6 +205,24 @@ void tp_reduce_norm(const GemmResult& g, OptT bias, OptT w, OptT out, double eps
   TORCH_CHECK(rc == 0, "tp_reduce_norm launch failed: rc=", rc);
 }
 
+// One-hop TP reduce for few rows (tp_comm.cu tp_local_norm_kernel).
+void tp_local_norm(const GemmResult& g, Tensor residual, OptT bias, OptT w, OptT out, double eps,
+                   int64_t W, int64_t gemm_flags, Tensor ctl, int64_t ctl_gemm_slot,
+                   int64_t ctl_done_slot, Tensor status, int64_t code, int64_t timeout_ns) {
+  CHECK_DT(residual, at::kFloat); CHECK_DT(ctl, at::kInt); CHECK_DT(status, at::kInt);
+  TORCH_CHECK(residual.size(-1) == g.g.rows && residual.size(0) >= g.g.T, "residual shape");
+  if (out.has_value()) CHECK_DT(*out, at::kHalf);
+  const at::cuda::CUDAGuard guard(ctl.device());
+  int* c = ctl.data_ptr<int>();
+  int rc = launch_tp_local_norm(g.g, residual.data_ptr<float>(), ptr_or_null<float>(bias),
+                                ptr_or_null<float>(w), ptr_or_null<__half>(out),
+                                out.has_value() ? (int)out->stride(0) : 0, (float)eps, (int)W,
+                                reinterpret_cast<const void*>(gemm_flags), c + ctl_gemm_slot,
+                                c + ctl_done_slot, status.data_ptr<int>(), (int)code,
+                                (long long)timeout_ns, cur_stream());
+  TORCH_CHECK(rc == 0, "tp_local_norm launch failed: rc=", rc);
+}
+
 void qgemm_set_trace_py(OptT buf) {
   if (buf.has_value()) TORCH_CHECK(buf->numel() * buf->element_size() >= 512 * 8 * 8, "trace buffer too small");
   qgemm_set_trace(ptr_or_null<void>(buf));
@@ -489,6 +507,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("src_stride"), py::arg("dst_ptrs"), py::arg("sig_ctl"), py::arg("sig_bases"),
         py::arg("sig_flag_off"), py::arg("rank"), py::arg("owner_tiles"), py::arg("fmt") = 0);
   m.def("tp_reduce_norm", &tp_reduce_norm);
+  m.def("tp_local_norm", &tp_local_norm);
   // Bounded wait for `world` epoch flags (flags: device address of uint32[world]);
   // timeout_ns <= 0 uses the kernels' default deadline (1 s).
   m.def("flag_wait", [](int64_t flags, int64_t world, Tensor ctl, int64_t slot, Tensor status,

@@ -150,7 +150,7 @@ int launch_moe_localize(int32_t* ids, float* wts, int* counts, int P, int E, int
 int launch_moe_combine_tp(const float* rows, int row_stride, const float* wts, int k,
                           const swarm::GemmOut* sh, const swarm::GemmOut* shg, int T, int H, int W,
                           const unsigned long long* dst, int* ctl, const unsigned long long* bases,
-                          long long flag_off, int rank, cudaStream_t s);
+                          long long flag_off, int rank, cudaStream_t s, int to_all = 0);
 
 void launch_mul_f16(__half* x, const __half* y, size_t n, cudaStream_t s);
 
@@ -200,6 +200,13 @@ int launch_tp_reduce_norm(const swarm::GemmOut& g, const float* bias, const floa
                           long long timeout_ns, cudaStream_t s);
 int launch_flag_wait(const void* flags, int world, int* ctl, int slot, int* status, int code,
                      cudaStream_t s, long long timeout_ns = 0);
+// One-hop TP reduce for few rows: every rank received every rank's partials
+// (GemmOut n_src = W); wait for the W GEMM-done flags, then residual += sum
+// (+ bias) in place and out = RMSNorm(residual) * w (w / out may be null).
+int launch_tp_local_norm(const swarm::GemmOut& g, float* residual, const float* bias,
+                         const float* w, __half* out, int out_stride, float eps, int W,
+                         const void* gemm_flags, int* ctl_gemm, int* ctl_done, int* status,
+                         int code, long long timeout_ns, cudaStream_t s);
 
 // GGML blocks -> fp16 [rows][K] (qmatmul_simt.cu); quantized types only.
 int launch_dequant_f16(const void* w, int type, int rows, int K, __half* out, cudaStream_t s);

@@ -573,7 +573,7 @@ __global__ void moe_localize_kernel(int32_t* __restrict__ ids, float* __restrict
 __global__ void __launch_bounds__(256) moe_combine_tp_kernel(
     const float* __restrict__ rows, int row_stride, const float* __restrict__ wts, int k,
     GemmOut sh, int has_sh, GemmOut shg, int has_shg, int H, int W, EpPeers dst, int* ctl,
-    EpPeers sig, long long flag_off, int rank) {
+    EpPeers sig, long long flag_off, int rank, int to_all) {
   const int t = blockIdx.x;
   const int per = H / W;
   float gate = 1.f;
@@ -585,7 +585,11 @@ __global__ void __launch_bounds__(256) moe_combine_tp_kernel(
       if (w != 0.f) v += w * rows[(size_t)(t * k + j) * row_stride + i];
     }
     if (has_sh) v += gate * sh.get(t, i);
-    reinterpret_cast<float*>(dst.base[i / per])[(size_t)t * H + i] = v;
+    if (to_all) {   // every rank sums every column itself (one-hop TP reduce)
+      for (int o = 0; o < W; ++o) reinterpret_cast<float*>(dst.base[o])[(size_t)t * H + i] = v;
+    } else {
+      reinterpret_cast<float*>(dst.base[i / per])[(size_t)t * H + i] = v;
+    }
   }
   ep_grid_done_signal(ctl, sig.base, flag_off, W, rank);
 }
@@ -863,7 +867,7 @@ int launch_moe_localize(int32_t* ids, float* wts, int* counts, int P, int E, int
 int launch_moe_combine_tp(const float* rows, int row_stride, const float* wts, int k,
                           const GemmOut* sh, const GemmOut* shg, int T, int H, int W,
                           const unsigned long long* dst, int* ctl, const unsigned long long* bases,
-                          long long flag_off, int rank, cudaStream_t s) {
+                          long long flag_off, int rank, cudaStream_t s, int to_all) {
   if (T <= 0) return 0;
   if (W < 1 || W > 8 || H % W) return -1;
   GemmOut z{};
@@ -874,6 +878,7 @@ int launch_moe_combine_tp(const float* rows, int row_stride, const float* wts, i
   }
   moe_combine_tp_kernel<<<T, 256, 0, s>>>(rows, row_stride, wts, k, sh ? *sh : z,
                                           (int)(sh != nullptr), shg ? *shg : z,
-                                          (int)(shg != nullptr), H, W, d, ctl, b, flag_off, rank);
+                                          (int)(shg != nullptr), H, W, d, ctl, b, flag_off, rank,
+                                          to_all);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }

@@ -43,6 +43,9 @@
 // and phase through a star or ring of network messages (src/inference/
 // allreduce.rs:63,413,620) and applies the residual and norm afterwards.
 #include "kernels.h"
+
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "ep_common.cuh"
 #include "gemm_out.cuh"
@@ -202,9 +205,156 @@ __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const TpReduceArgs 
   }
 }
 
+// One-hop variant for few rows (decode): the row-parallel GEMM stored its
+// partial tiles into EVERY rank's receive buffer, so each rank sums all W
+// partials of every column itself -- the same additions in the same order on
+// every rank, so the replicated residual stays bitwise identical -- and the
+// only cross-GPU dependency is the GEMM-done flags.  One row per cluster of
+// kTpCluster CTAs (distributed shared memory sums the squares), as the
+// single-GPU residual + RMSNorm epilogue.
+constexpr int kTpCluster = 8;
+namespace cg = cooperative_groups;
+
+struct TpLocalArgs {
+  GemmOut g;                 // n_src = W sources in this rank's receive buffer
+  float* residual;           // [T][H], updated in place
+  const float* bias;
+  const float* w;            // RMSNorm weight, or null: residual update only
+  __half* out;
+  int out_stride;
+  float eps;
+  int W;
+  const uint32_t* gemm_flags;
+  int* ctl_gemm;             // [0]: last GEMM-done epoch waited for
+  int* ctl_done;             // [0]: done-CTA counter
+  int* status;
+  int code;
+  unsigned long long timeout_ns;
+};
+
+__global__ void __launch_bounds__(256) tp_local_norm_kernel(const TpLocalArgs a) {
+  pdl_trigger();
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float part;
+  __shared__ float red[32];
+  __shared__ int ok_s;
+  extern __shared__ float slice[];
+  const uint32_t want = (uint32_t)a.ctl_gemm[0] + 1;
+  const unsigned long long t0 = tc::globaltimer();
+  if (threadIdx.x == 0) ok_s = 1;
+  __syncthreads();
+  if (threadIdx.x < a.W && !wait_ge(a.gemm_flags + threadIdx.x, want, t0, a.timeout_ns)) {
+    ok_s = 0;
+    record_fail(a.status, a.code, threadIdx.x, (int)want, -2);
+  }
+  __syncthreads();
+  const bool ok = ok_s != 0;
+  const int cr = (int)cluster.block_rank(), cn = (int)cluster.num_blocks();
+  const int t = blockIdx.x / cn;
+  const int dim = a.g.rows;
+  const int per = (dim + cn - 1) / cn;
+  const int lo = cr * per, hi = min(dim, lo + per);
+  float* rr = a.residual + (size_t)t * dim;
+  float ss = 0.f;
+  if (ok) {
+    for (int i = lo + 8 * threadIdx.x; i < hi; i += 8 * blockDim.x) {
+      float4 v0, v1;
+      a.g.get8(t, i, v0, v1);
+      v0 = add4(v0, *reinterpret_cast<const float4*>(rr + i));
+      v1 = add4(v1, *reinterpret_cast<const float4*>(rr + i + 4));
+      if (a.bias) {
+        v0 = add4(v0, *reinterpret_cast<const float4*>(a.bias + i));
+        v1 = add4(v1, *reinterpret_cast<const float4*>(a.bias + i + 4));
+      }
+      *reinterpret_cast<float4*>(rr + i) = v0;
+      *reinterpret_cast<float4*>(rr + i + 4) = v1;
+      *reinterpret_cast<float4*>(slice + (i - lo)) = v0;
+      *reinterpret_cast<float4*>(slice + (i - lo) + 4) = v1;
+      ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w + v1.x * v1.x + v1.y * v1.y +
+            v1.z * v1.z + v1.w * v1.w;
+    }
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) part = ss;
+  cluster.sync();
+  float tot = 0.f;
+  for (int r = 0; r < cn; ++r) tot += *cluster.map_shared_rank(&part, r);
+  cluster.sync();  // peers finished reading `part` before any CTA exits
+  if (ok && a.out != nullptr && a.w != nullptr) {
+    const float inv = rsqrtf(tot / dim + a.eps);
+    __half* o = a.out + (size_t)t * a.out_stride;
+    for (int i = lo + 8 * threadIdx.x; i < hi; i += 8 * blockDim.x) {
+      const float4 v0 = *reinterpret_cast<const float4*>(slice + (i - lo));
+      const float4 v1 = *reinterpret_cast<const float4*>(slice + (i - lo) + 4);
+      const float4 w0 = *reinterpret_cast<const float4*>(a.w + i);
+      const float4 w1 = *reinterpret_cast<const float4*>(a.w + i + 4);
+      __half2 r[4];
+      r[0] = __floats2half2_rn(v0.x * inv * w0.x, v0.y * inv * w0.y);
+      r[1] = __floats2half2_rn(v0.z * inv * w0.z, v0.w * inv * w0.w);
+      r[2] = __floats2half2_rn(v1.x * inv * w1.x, v1.y * inv * w1.y);
+      r[3] = __floats2half2_rn(v1.z * inv * w1.z, v1.w * inv * w1.w);
+      *reinterpret_cast<uint4*>(o + i) = *reinterpret_cast<const uint4*>(r);
+    }
+  }
+  // the last CTA advances the wait epoch (every CTA has read it by then)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&a.ctl_done[0], 1);
+    if (prev == (int)gridDim.x - 1) {
+      a.ctl_done[0] = 0;
+      a.ctl_gemm[0] = (int)want;
+    }
+  }
+}
+
 }  // namespace swarm
 
 using namespace swarm;
+
+int launch_tp_local_norm(const GemmOut& g, float* residual, const float* bias, const float* w,
+                         __half* out, int out_stride, float eps, int W, const void* gemm_flags,
+                         int* ctl_gemm, int* ctl_done, int* status, int code,
+                         long long timeout_ns, cudaStream_t s) {
+  if (g.T <= 0) return 0;
+  const int dim = g.rows;
+  if (W < 1 || W > 8 || g.n_src != W || dim % (8 * kTpCluster) != 0) return -1;
+  if (out && ((out_stride % 8) != 0 || (reinterpret_cast<uintptr_t>(out) & 15) != 0)) return -3;
+  TpLocalArgs a{};
+  a.g = g;
+  a.residual = residual;
+  a.bias = bias;
+  a.w = w;
+  a.out = out;
+  a.out_stride = out_stride ? out_stride : dim;
+  a.eps = eps;
+  a.W = W;
+  a.gemm_flags = static_cast<const uint32_t*>(gemm_flags);
+  a.ctl_gemm = ctl_gemm;
+  a.ctl_done = ctl_done;
+  a.status = status;
+  a.code = code;
+  a.timeout_ns = timeout_ns > 0 ? (unsigned long long)timeout_ns : tc::kWaitTimeoutNs;
+  const int per = dim / kTpCluster;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g.T * kTpCluster);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = (size_t)per * sizeof(float);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kTpCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if ((size_t)per * sizeof(float) > 48 * 1024 &&
+      cudaFuncSetAttribute(tp_local_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(per * sizeof(float))) != cudaSuccess)
+    return -4;
+  if (cudaLaunchKernelEx(&cfg, tp_local_norm_kernel, a) != cudaSuccess) return -4;
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
 
 int tp_reduce_slices(int T, int H, int W, int num_sms) {
   // CTAs per row: fill about two CTAs per SM, each slice a whole number of

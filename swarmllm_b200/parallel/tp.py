@@ -18,6 +18,12 @@ into two kernels over NVLink peer memory, with no collective call:
 Per row-parallel layer each rank sends (W-1)/W of its partial result once and
 its residual slice W-1 times; there is no all-gather of partials.
 
+For few rows (decode: T * (W - 1) <= SWARMLLM_TP_LOCAL_ROWS, default 32) the
+two cross-GPU hops of that scheme cost more than the bytes: the GEMM then
+stores every tile into every rank's buffer and `tp_local_norm` sums all W
+partials of every column locally (same order on every rank, so the
+replicated residual stays identical), waiting only on the GEMM-done flags.
+
 Arena (CUDA-IPC mapped, identical offsets on every rank), in bytes:
   recv      [2][W][ws]      fp32 partials per source rank (2 alternating buffers)
   gemm flag [2][W]          u32 GEMM-done epochs, one word per source rank
@@ -35,6 +41,8 @@ Reference behaviour: the reference's TP splits heads and FFN columns
 the network per layer and phase (src/inference/allreduce.rs:63,413,620).
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -54,6 +62,8 @@ class TpGroup:
     # Status codes of the waits (GEMM-done flags; +1: row-slice flags)
     CODE_REDUCE = 73
     MAX_SLICES = 16  # CTAs per row of tp_reduce_norm (tp_comm.cu tp_reduce_slices)
+    # one-hop reduce (partials to every rank) while T * (W - 1) is at most this
+    LOCAL_ROWS = int(os.environ.get("SWARMLLM_TP_LOCAL_ROWS", "32"))
 
     def __init__(self, rank: int, world: int, device, group=None, timeout_ns: int = 0):
         assert 1 <= world <= 8
@@ -102,13 +112,17 @@ class TpGroup:
     def begin_forward(self):
         self.k = 0
 
+    def local(self, T: int) -> bool:
+        """Whether T rows take the one-hop reduce (every rank sums every column)."""
+        return T * (self.world - 1) <= self.LOCAL_ROWS
+
     def row_parallel(self, lin, x: torch.Tensor, status: torch.Tensor, num_sms: int):
         """GEMM of a K-split Q4_K weight; each result tile goes to its owner rank."""
         b = self.k & 1
         W, r = self.world, self.rank
         own = self.base + (b * W) * self.ws_bytes
         dsts = [self.bases[o] + (b * W + r) * self.ws_bytes for o in range(W)]
-        owner_tiles = self.H // 128 // W
+        owner_tiles = 0 if self.local(x.shape[0]) else self.H // 128 // W
         return C().qgemm_q4k_tc_tp(lin.packed, lin.rows, lin.K, x, status, num_sms, own,
                                    self.ws_bytes // 4, dsts, self.ctl[4 * b:], self.bases,
                                    self.flag_off + b * W * 4, r, owner_tiles, lin.fmt)
@@ -123,7 +137,7 @@ class TpGroup:
         dsts = [self.bases[o] + (b * W + r) * self.ws_bytes for o in range(W)]
         return C().moe_combine_tp(rows, wts, k, shared, shared_gate, T, self.H, own,
                                   self.ws_bytes // 4, dsts, self.ctl[4 * b:], self.bases,
-                                  self.flag_off + b * W * 4, r)
+                                  self.flag_off + b * W * 4, r, self.local(T))
 
     def reduce_norm(self, g, bias, w, out, eps: float, status: torch.Tensor, num_sms: int):
         """Residual += sum over ranks of the row-parallel result (+ bias), then
@@ -132,6 +146,14 @@ class TpGroup:
         b = k & 1
         T = g.T
         assert T <= self.t_max
+        if self.local(T):
+            # residual updated in place in buffer 1 (h_view), where a forward
+            # of slice-path calls also starts and ends
+            C().tp_local_norm(g, self.h_view()[:T], bias, w, out, eps, W,
+                              self.base + self.flag_off + b * W * 4, self.ctl, 4 * b + 2, 8,
+                              status, self.CODE_REDUCE, self.timeout_ns)
+            self.k += 1
+            return
         C().tp_reduce_norm(g, bias, w, out, eps, self.H, self.rank, T, self.t_max, self.bases,
                            self.h_off + ((k + 1) & 1) * self.h_bytes,
                            self.h_off + b * self.h_bytes,

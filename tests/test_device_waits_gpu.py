@@ -57,7 +57,10 @@ def _one_rank_group():
     return True
 
 
-def test_tp_reduce_numerics_and_timeout_one_rank():
+@pytest.mark.parametrize("one_hop", [False, True])
+def test_tp_reduce_numerics_and_timeout_one_rank(one_hop):
+    """Both reduce paths: the reduce-scatter + all-gather slices
+    (tp_reduce_norm) and the one-hop local sum (tp_local_norm)."""
     import torch.distributed as dist
     from swarmllm_b200.gguf import quants as Q
     from swarmllm_b200.ops.linear import GemmWorkspace, QLinear, stream_k_floats
@@ -71,6 +74,8 @@ def test_tp_reduce_numerics_and_timeout_one_rank():
         lin = QLinear(wq, Q.Q4_K, H, K, DEV)
         ws = GemmWorkspace(DEV, T, H)
         tp = TpGroup(0, 1, DEV, timeout_ns=TIMEOUT_NS)
+        tp.LOCAL_ROWS = 10 ** 6 if one_hop else -1
+        assert tp.local(T) == one_hop
         tp.setup(stream_k_floats(T, H, ws.num_sms), T, H)
         h = tp.h_view()
         h0 = torch.randn(T, H, device=DEV)

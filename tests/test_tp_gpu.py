@@ -1,5 +1,7 @@
 """Tensor parallelism with the fused GEMM + peer-memory reduction (2 GPUs):
-the TP2 model's logits equal the single-GPU model's.  Skipped with fewer
+the TP2 model's logits equal the single-GPU model's, for a dense Llama and a
+Qwen3-Next-like hybrid (DeltaNet heads, gated attention, experts + shared
+expert), at prefill and at decode (both reduce paths).  Skipped with fewer
 than two GPUs."""
 import os
 import socket
@@ -20,14 +22,34 @@ def _free_port():
     return p
 
 
-def _batch(tokens, positions, bt, device, sample_rows):
+def _batch(tokens, positions, bt, device, sample_rows, hybrid=False):
     from swarmllm_b200.models.llama import StepBatch
     t = lambda a, dt=torch.int32: torch.as_tensor(np.asarray(a), dtype=dt, device=device)
-    return StepBatch(t(tokens), t(positions), t(positions), t(bt), t(np.asarray(positions) + 1),
-                     t(sample_rows, torch.int64), 256)
+    b = StepBatch(t(tokens), t(positions), t(positions), t(bt), t(np.asarray(positions) + 1),
+                  t(sample_rows, torch.int64), 256)
+    if hybrid:   # one sequence in recurrent-state slot 0
+        b.ssm_seqs = t([[0, len(tokens), 0, int(positions[0])]])
+        b.ssm_max_rows = len(tokens)
+    return b
 
 
-def _worker(rank, world, port):
+def _cfg(kind):
+    from swarmllm_b200.models.config import ModelConfig
+    if kind == "dense":
+        return ModelConfig(name="t", arch="llama", n_layers=3, hidden=512, n_heads=8,
+                           n_kv_heads=2, head_dim=64, ffn=1024, vocab=1024, weight_qtype="Q4_K",
+                           embed_qtype="F16", output_qtype="Q4_K")
+    return ModelConfig(name="t-hybrid", arch="qwen3next", n_layers=4, hidden=512, n_heads=4,
+                       n_kv_heads=2, head_dim=256, ffn=512, vocab=1024, rope_theta=1e7,
+                       rope_neox=True, rope_dim=64, rms_eps=1e-6, qk_norm=True,
+                       attn_output_gate=True, n_experts=8, n_experts_used=2, expert_ffn=256,
+                       shared_expert_ffn=512, moe_softmax_after_topk=True,
+                       full_attn_interval=4, ssm_k_heads=2, ssm_v_heads=8, ssm_head_dim=128,
+                       ssm_conv_kernel=4, weight_qtype="Q4_K", embed_qtype="F16",
+                       output_qtype="Q4_K", expert_qtype="Q4_K")
+
+
+def _worker(rank, world, port, kind="dense"):
     import torch.distributed as dist
     from swarmllm_b200.models.config import ModelConfig
     from swarmllm_b200.models.llama import LlamaGPU
@@ -41,15 +63,18 @@ def _worker(rank, world, port):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=dev)
     try:
-        cfg = ModelConfig(name="t", arch="llama", n_layers=3, hidden=512, n_heads=8, n_kv_heads=2,
-                          head_dim=64, ffn=1024, vocab=1024, weight_qtype="Q4_K",
-                          embed_qtype="F16", output_qtype="Q4_K")
+        cfg = _cfg(kind)
+        hybrid = kind == "hybrid"
         tp = TpGroup(rank, world, dev)
         m_tp = LlamaGPU(cfg, RandomSource(cfg, seed=3), dev, tp=tp)
         m_1 = LlamaGPU(cfg, RandomSource(cfg, seed=3), dev)
         c_tp, c_1 = m_tp.make_context(128, 128, 256), m_1.make_context(128, 128, 256)
         kv_tp = PagedKVCache(cfg.n_layers, 8, m_tp.n_kv, cfg.head_dim, dev)
         kv_1 = PagedKVCache(cfg.n_layers, 8, cfg.n_kv_heads, cfg.head_dim, dev)
+        if hybrid:
+            for m, kv in ((m_tp, kv_tp), (m_1, kv_1)):
+                n, nv, dk, dv, ch, ck = m.linear_state_spec()
+                kv.add_linear_state(n, 1, nv, dk, dv, ch, ck)
         rng = np.random.default_rng(0)
         toks = rng.integers(0, cfg.vocab, 83)
         bt = np.tile(np.arange(8, dtype=np.int32), (128, 1))
@@ -58,23 +83,25 @@ def _worker(rank, world, port):
         for lo, hi in ((0, 80), (80, 81), (81, 82), (82, 83)):
             pos = np.arange(lo, hi)
             rows = list(range(hi - lo))
-            a = m_tp.forward(_batch(toks[lo:hi], pos, bt[:hi - lo], dev, rows), kv_tp, c_tp)
-            b = m_1.forward(_batch(toks[lo:hi], pos, bt[:hi - lo], dev, rows), kv_1, c_1)
+            a = m_tp.forward(_batch(toks[lo:hi], pos, bt[:hi - lo], dev, rows, hybrid), kv_tp, c_tp)
+            b = m_1.forward(_batch(toks[lo:hi], pos, bt[:hi - lo], dev, rows, hybrid), kv_1, c_1)
             torch.cuda.synchronize(dev)
             c_tp.gemm.check()
             cos = torch.nn.functional.cosine_similarity(a.double(), b.double(), dim=-1)
             assert float(cos.min()) > 0.9999, (rank, lo, cos)
             rel = float((a - b).norm() / b.norm())
             # fp32 partials summed in another order change which fp16 activations
-            # round up; over 3 layers that moves the logits by ~1e-3
-            assert rel < 3e-3, (rank, lo, rel)
+            # round up (and, at one decode row, which int8 activation steps the
+            # GEMV picks); over 3-4 layers that moves the logits by up to ~6e-3
+            assert rel < 1.2e-2, (rank, lo, rel)
         tp.close()
     finally:
         dist.destroy_process_group()
 
 
-def test_tp2_matches_single_gpu():
+@pytest.mark.parametrize("kind", ["dense", "hybrid"])
+def test_tp2_matches_single_gpu(kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
-    mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), kind), nprocs=2, join=True)
