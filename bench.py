@@ -334,7 +334,18 @@ def tensor_parallel(args):
     dist.destroy_process_group()
 
 
+def _json_only_stdout():
+    """Keep stdout for the result line: libraries that write to file
+    descriptor 1 from C (NCCL's version banner, for one) go to stderr, and
+    Python's sys.stdout keeps a private handle on the real stdout."""
+    sys.stdout.flush()
+    real = os.fdopen(os.dup(1), "w", buffering=1)
+    os.dup2(2, 1)
+    sys.stdout = real
+
+
 def main():
+    _json_only_stdout()
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)

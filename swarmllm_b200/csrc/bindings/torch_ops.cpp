@@ -508,6 +508,23 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sig_flag_off"), py::arg("rank"), py::arg("owner_tiles"), py::arg("fmt") = 0);
   m.def("tp_reduce_norm", &tp_reduce_norm);
   m.def("tp_local_norm", &tp_local_norm);
+  m.def("mma_probe_shapes", []() {
+    std::vector<std::tuple<int, int, int>> v;
+    for (int i = 0; i < mma_probe_shapes(); ++i) {
+      int ts, mm, nn;
+      mma_probe_shape(i, &ts, &mm, &nn);
+      v.emplace_back(ts, mm, nn);
+    }
+    return v;
+  });
+  m.def("mma_probe", [](int64_t shape, int64_t iters, Tensor cycles) {
+    CHECK_DT(cycles, at::kLong);
+    const at::cuda::CUDAGuard guard(cycles.device());
+    TORCH_CHECK(launch_mma_probe((int)shape, (int)iters, (int)cycles.numel(),
+                                 cycles.data_ptr<int64_t>() ? reinterpret_cast<long long*>(
+                                     cycles.data_ptr<int64_t>()) : nullptr,
+                                 cur_stream()) == 0, "mma_probe launch failed");
+  });
   // Bounded wait for `world` epoch flags (flags: device address of uint32[world]);
   // timeout_ns <= 0 uses the kernels' default deadline (1 s).
   m.def("flag_wait", [](int64_t flags, int64_t world, Tensor ctl, int64_t slot, Tensor status,

@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(192, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
                    const __grid_constant__ CUtensorMap v_map, AttnTcArgs a) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   using C = AttnCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -582,12 +583,14 @@ static int launch_d(const CUtensorMap& qm, const CUtensorMap& km, const CUtensor
       !smem_attr_once(attn_tc_kernel<D, false, 4>, C::SMEM, &done4))
     return -3;
   dim3 grid(G, a.n_kv, a.n_splits);
+  cudaError_t e;
   if (a.tree_mask != nullptr)
-    attn_tc_kernel<D, true, 1><<<grid, C::THREADS, C::SMEM, s>>>(qm, km, vm, a);
+    e = launch_pdl(attn_tc_kernel<D, true, 1>, grid, dim3(C::THREADS), C::SMEM, s, qm, km, vm, a);
   else if (a.n_rep * a.pos_per_group == 8)  // 8-row groups (decode, 8 heads per KV head)
-    attn_tc_kernel<D, false, 4><<<grid, C::THREADS, C::SMEM, s>>>(qm, km, vm, a);
+    e = launch_pdl(attn_tc_kernel<D, false, 4>, grid, dim3(C::THREADS), C::SMEM, s, qm, km, vm, a);
   else
-    attn_tc_kernel<D, false, 1><<<grid, C::THREADS, C::SMEM, s>>>(qm, km, vm, a);
+    e = launch_pdl(attn_tc_kernel<D, false, 1>, grid, dim3(C::THREADS), C::SMEM, s, qm, km, vm, a);
+  if (e != cudaSuccess) return -4;
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

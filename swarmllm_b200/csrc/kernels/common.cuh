@@ -17,14 +17,16 @@ namespace swarm {
 
 constexpr int kWarp = 32;
 
-// Programmatic dependent launch (PDL).  The weight-streaming GEMM / GEMV
-// kernels are launched with programmatic stream serialisation: they may start
-// while the kernel before them is still running, stream their first weight
-// tiles, and call pdl_wait() before reading activations or writing results
-// (it returns once the previous grid has completed and its writes are
-// visible).  The kernels that usually precede them call pdl_trigger() first
-// thing, which lets the dependent grid launch as soon as every CTA of the
-// current grid is running.  Both are no-ops for launches without the attribute.
+// Programmatic dependent launch (PDL).  The decode-path kernels are launched
+// with programmatic stream serialisation: they may start while the kernel
+// before them is still running.  Every kernel calls pdl_trigger() first thing,
+// which lets the next grid launch as soon as every CTA of the current one is
+// running, and pdl_wait() before it reads anything an earlier kernel wrote
+// (it returns once the previous grid -- and through it every earlier one --
+// has completed and its writes are visible).  The weight-streaming GEMMs
+// stream their first weight tiles before waiting; the epilogue-type kernels
+// wait at once, so they only hide their launch latency.  Both calls are
+// no-ops for launches without the attribute.
 SW_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 SW_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
@@ -45,6 +47,35 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
+// The same with a thread-block cluster of `cluster_x` CTAs (1: none).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                                      size_t smem, cudaStream_t s, int cluster_x,
+                                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
 }
 

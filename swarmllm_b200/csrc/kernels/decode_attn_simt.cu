@@ -40,6 +40,7 @@ struct DecodeAttnArgs {
 template <int D, int NREP>
 __global__ void __launch_bounds__(128) decode_attn_split_kernel(DecodeAttnArgs a) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   const int t = blockIdx.x, hk = blockIdx.y, sp = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int L = a.seq_lens[t];
@@ -151,6 +152,7 @@ __global__ void decode_attn_combine_kernel(const float* __restrict__ part_o,
                                            const float* __restrict__ sinks, int n_q,
                                            __half* __restrict__ out) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   const int row = blockIdx.x;  // t * n_q + h
   const int h = row % n_q;
   const float* ml = part_ml + (size_t)row * n_splits * 2;
@@ -180,7 +182,7 @@ static int dispatch_nrep(const DecodeAttnArgs& a, int nrep, int T, cudaStream_t 
     if (sm > 48 * 1024)                                                                 \
       cudaFuncSetAttribute(decode_attn_split_kernel<D, R>,                              \
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);       \
-    decode_attn_split_kernel<D, R><<<grid, 128, sm, s>>>(a);                            \
+    launch_pdl(decode_attn_split_kernel<D, R>, grid, dim3(128), sm, s, a);              \
     break;
   switch (nrep) {
     SW_CASE(1) SW_CASE(2) SW_CASE(3) SW_CASE(4) SW_CASE(5) SW_CASE(6) SW_CASE(8)
@@ -216,8 +218,8 @@ int launch_decode_attn_simt(const __half* q, const __half* k_cache, const __half
     default: return -1;
   }
   if (rc) return rc;
-  decode_attn_combine_kernel<<<T * n_q, 128, 0, s>>>(part_o, part_ml, n_splits, head_dim, sinks,
-                                                    n_q, out);
+  launch_pdl(decode_attn_combine_kernel, dim3(T * n_q), dim3(128), 0, s, part_o, part_ml,
+             n_splits, head_dim, sinks, n_q, out);
   SW_LAUNCH_CHECK();
   return 0;
 }
@@ -226,6 +228,7 @@ int launch_decode_attn_simt(const __half* q, const __half* k_cache, const __half
 void launch_attn_combine(const float* part_o, const float* part_ml, int rows, int n_splits, int D,
                          const float* sinks, int n_q, __half* out, cudaStream_t s) {
   if (rows <= 0) return;
-  decode_attn_combine_kernel<<<rows, 128, 0, s>>>(part_o, part_ml, n_splits, D, sinks, n_q, out);
+  launch_pdl(decode_attn_combine_kernel, dim3(rows), dim3(128), 0, s, part_o, part_ml, n_splits,
+             D, sinks, n_q, out);
   SW_LAUNCH_CHECK();
 }

@@ -48,6 +48,7 @@ __global__ void ssm_conv_silu_kernel(GemmOut g, const float* __restrict__ w, int
                                      const int4* __restrict__ seqs, int S,
                                      float* __restrict__ out) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   const int r = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
@@ -105,6 +106,7 @@ __global__ void __launch_bounds__(D) delta_rule_kernel(
     const float* __restrict__ norm_w, float eps, float* __restrict__ state,
     const int4* __restrict__ seqs, __half* __restrict__ out) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   static_assert(D == 128, "one thread per value channel, 4 warps");
   __shared__ float qs[D], ks[D], red[8];
   const int s = blockIdx.x, h = blockIdx.y, j = threadIdx.x;

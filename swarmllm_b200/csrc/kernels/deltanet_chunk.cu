@@ -289,6 +289,7 @@ __global__ void gated_norm_kernel(const float* __restrict__ o_raw, GemmOut gz,
                                   const float* __restrict__ norm_w, float eps, int T, int nv,
                                   __half* __restrict__ out) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   const int idx = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (idx >= T * nv) return;

@@ -28,6 +28,7 @@ namespace swarm {
 __global__ void embed_gather_kernel(const uint8_t* __restrict__ table, int type, int hidden,
                                     const int32_t* __restrict__ ids, float* __restrict__ out) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   const int t = blockIdx.x;
   const int id = ids[t];
   const int bv = ggml_block_values(type), bb = ggml_block_bytes(type);
@@ -43,6 +44,7 @@ template <int kThreads>
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                __half* __restrict__ out, int dim, float eps) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   __shared__ float red[32];
   const int t = blockIdx.x;
   const float* xr = x + (size_t)t * dim;
@@ -63,6 +65,7 @@ __global__ void epi_residual_rmsnorm_kernel(GemmOut g, float* __restrict__ resid
                                             __half* __restrict__ out, float eps,
                                             int out_stride) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   extern __shared__ float row[];
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -150,6 +153,7 @@ __global__ void epi_postnorm_residual_rmsnorm_kernel(GemmOut g, float* __restric
                                                      __half* __restrict__ out, float eps,
                                                      int out_stride) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   extern __shared__ float row[];
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -193,6 +197,8 @@ __global__ void epi_rope_kv_kernel(GemmOut g, const float* __restrict__ bias,
                                    const float* __restrict__ q_norm_w,
                                    const float* __restrict__ k_norm_w, float norm_eps,
                                    __half* __restrict__ gate_out) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   extern __shared__ float sh[];  // kRopeHpb * head_dim floats
   const int t = blockIdx.x;
   const int h0 = blockIdx.y * kRopeHpb;
@@ -356,6 +362,7 @@ __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int
                                   int interleaved, float alpha, float limit,
                                   __half* __restrict__ out) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   const int t = blockIdx.y;
   if (!interleaved && (F & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
     // eight features per thread and step: one partial-sum lookup per eight, 16-byte stores
@@ -429,6 +436,8 @@ __global__ void epi_swiglu_kernel(GemmOut g, const float* __restrict__ bias, int
 
 __global__ void epi_copy_kernel(GemmOut g, const float* __restrict__ bias, float* __restrict__ out,
                                 int out_stride) {
+  pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   const int t = blockIdx.y;
   if ((g.rows & 3) == 0 && (out_stride & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
     for (int i = 4 * (blockIdx.x * blockDim.x + threadIdx.x); i < g.rows;
@@ -450,6 +459,7 @@ __global__ void epi_copy_kernel(GemmOut g, const float* __restrict__ bias, float
 
 __global__ void mul_f16_kernel(__half* __restrict__ x, const __half* __restrict__ y, size_t n) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     x[i] = __hmul(x[i], y[i]);
@@ -469,14 +479,15 @@ using namespace swarm;
 void launch_embed_gather(const void* table, int type, int hidden, const int32_t* ids, int n,
                          float* out, cudaStream_t s) {
   if (n <= 0) return;
-  embed_gather_kernel<<<n, 256, 0, s>>>((const uint8_t*)table, type, hidden, ids, out);
+  launch_pdl(embed_gather_kernel, dim3(n), dim3(256), 0, s, (const uint8_t*)table, type, hidden,
+             ids, out);
   SW_LAUNCH_CHECK();
 }
 
 void launch_rmsnorm(const float* x, const float* w, __half* out, int rows, int dim,
                     float eps, cudaStream_t s) {
   if (rows <= 0) return;
-  rmsnorm_kernel<512><<<rows, 512, 0, s>>>(x, w, out, dim, eps);
+  launch_pdl(rmsnorm_kernel<512>, dim3(rows), dim3(512), 0, s, x, w, out, dim, eps);
   SW_LAUNCH_CHECK();
 }
 
@@ -490,6 +501,7 @@ __global__ void __launch_bounds__(256) epi_residual_rmsnorm_cluster_kernel(
     GemmOut g, float* __restrict__ residual, const float* __restrict__ bias,
     const float* __restrict__ w, __half* __restrict__ out, float eps, int out_stride) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float part;
   __shared__ float red[32];
@@ -528,27 +540,16 @@ void launch_epi_residual_rmsnorm(const GemmOut& g, float* residual, const float*
     if (sm > 48 * 1024)
       cudaFuncSetAttribute(epi_postnorm_residual_rmsnorm_kernel<512>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    epi_postnorm_residual_rmsnorm_kernel<512><<<g.T, 512, sm, s>>>(
-        g, residual, bias, post_w, w, out, eps, out_stride ? out_stride : g.rows);
+    launch_pdl(epi_postnorm_residual_rmsnorm_kernel<512>, dim3(g.T), dim3(512), sm, s, g,
+               residual, bias, post_w, w, out, eps, out_stride ? out_stride : g.rows);
     SW_LAUNCH_CHECK();
     return;
   }
   if (g.T < 64) {
     const int per = (g.rows + kClusterNorm - 1) / kClusterNorm;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(g.T * kClusterNorm);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = (size_t)per * sizeof(float);
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kClusterNorm;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, epi_residual_rmsnorm_cluster_kernel, g, residual, bias, w, out, eps,
-                       out_stride ? out_stride : g.rows);
+    launch_pdl_cluster(epi_residual_rmsnorm_cluster_kernel, dim3(g.T * kClusterNorm), dim3(256),
+                       (size_t)per * sizeof(float), s, kClusterNorm, g, residual, bias, w, out,
+                       eps, out_stride ? out_stride : g.rows);
     SW_LAUNCH_CHECK();
     return;
   }
@@ -556,8 +557,8 @@ void launch_epi_residual_rmsnorm(const GemmOut& g, float* residual, const float*
   if (sm > 48 * 1024)
     cudaFuncSetAttribute(epi_residual_rmsnorm_kernel<512>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  epi_residual_rmsnorm_kernel<512><<<g.T, 512, sm, s>>>(g, residual, bias, w, out, eps,
-                                                        out_stride ? out_stride : g.rows);
+  launch_pdl(epi_residual_rmsnorm_kernel<512>, dim3(g.T), dim3(512), sm, s, g, residual, bias, w,
+             out, eps, out_stride ? out_stride : g.rows);
   SW_LAUNCH_CHECK();
 }
 
@@ -570,9 +571,9 @@ void launch_epi_rope_kv(const GemmOut& g, const float* bias, const int32_t* posi
   if (g.T <= 0) return;
   const size_t sm = (size_t)kRopeHpb * head_dim * sizeof(float);
   const int groups = (n_q + 2 * n_kv + kRopeHpb - 1) / kRopeHpb;
-  epi_rope_kv_kernel<<<dim3(g.T, groups), 256, sm, s>>>(
-      g, bias, positions, slots, inv_freq, n_q, n_kv, head_dim, rope_dim, neox, attn_factor,
-      q_out, k_cache, v_cache, page_size, q_norm_w, k_norm_w, norm_eps, gate_out);
+  launch_pdl(epi_rope_kv_kernel, dim3(g.T, groups), dim3(256), sm, s, g, bias, positions, slots,
+             inv_freq, n_q, n_kv, head_dim, rope_dim, neox, attn_factor, q_out, k_cache, v_cache,
+             page_size, q_norm_w, k_norm_w, norm_eps, gate_out);
   SW_LAUNCH_CHECK();
 }
 
@@ -583,7 +584,8 @@ void launch_epi_swiglu(const GemmOut& g, const float* bias, int F, int kind, int
   const int per = (!interleaved && (F & 7) == 0) ? 8 : (!interleaved && (F & 3) == 0) ? 4 : 1;
   const int need = (F + per * 256 - 1) / (per * 256);
   dim3 grid(need < 64 ? need : 64, g.T);
-  epi_swiglu_kernel<<<grid, 256, 0, s>>>(g, bias, F, kind, interleaved, alpha, limit, out);
+  launch_pdl(epi_swiglu_kernel, grid, dim3(256), 0, s, g, bias, F, kind, interleaved, alpha,
+             limit, out);
   SW_LAUNCH_CHECK();
 }
 
@@ -591,7 +593,8 @@ void launch_epi_copy(const GemmOut& g, const float* bias, float* out, int out_st
                      cudaStream_t s) {
   if (g.T <= 0) return;
   dim3 grid((g.rows + 255) / 256 < 256 ? (g.rows + 255) / 256 : 256, g.T);
-  epi_copy_kernel<<<grid, 256, 0, s>>>(g, bias, out, out_stride ? out_stride : g.rows);
+  launch_pdl(epi_copy_kernel, grid, dim3(256), 0, s, g, bias, out,
+             out_stride ? out_stride : g.rows);
   SW_LAUNCH_CHECK();
 }
 

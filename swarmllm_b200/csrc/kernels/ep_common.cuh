@@ -30,12 +30,15 @@ SW_DEVICE void ep_signal_all(const unsigned long long* bases, long long flag_off
 
 // "Last CTA done" completion signal: every thread of every CTA calls this at
 // the very end; the CTA that finishes last raises the flags.  `ctl[0]` is the
-// done counter, `ctl[1]` the epoch.
+// done counter, `ctl[1]` the epoch.  One system-scope fence per CTA, after
+// the CTA barrier, publishes all of the CTA's stores (peer stores included)
+// before its count: the barrier orders the other threads' stores before
+// thread 0's fence, which is cumulative.
 SW_DEVICE void ep_grid_done_signal(int* ctl, const unsigned long long* bases, long long flag_off,
                                    int world, int rank) {
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const int prev = atomicAdd(&ctl[0], 1);
     if (prev == (int)(gridDim.x * gridDim.y * gridDim.z) - 1) {
       ctl[0] = 0;

@@ -1,0 +1,117 @@
+// Diagnostics: the issue rate of tcgen05.mma kind::f16 shapes.
+//
+// One CTA per SM issues `iters` x 4 MMAs of one shape (M x N x 16, fp16 in,
+// fp32 accumulate) back to back from one thread, commits once and waits; the
+// clock64 difference per MMA is what a weight-streaming GEMM pays per
+// instruction.  Operands are whatever shared memory / TMEM holds (the values
+// do not matter), laid out as the GEMMs lay theirs out: K-major, 128-byte
+// swizzle, 8-row groups of 1024 bytes, four K = 16 steps inside one 128-byte
+// row.  TS = A from TMEM (the quantized GEMM's form), SS = A from shared memory.
+#include "kernels.h"
+
+#include "common.cuh"
+#include "tc_utils.cuh"
+
+namespace swarm {
+using namespace tc;
+
+template <bool TS, int M, int N>
+struct ProbeCfg {
+  static constexpr int A_BYTES = TS ? 0 : M * 128;
+  static constexpr int B_BYTES = N * 128;
+  static constexpr int SMEM = 1024 + A_BYTES + B_BYTES + 64;
+  static constexpr int NEED = N + (TS ? 32 : 0);   // D columns (+ A for TS)
+  static constexpr int COLS = NEED <= 32 ? 32 : NEED <= 64 ? 64 : NEED <= 128 ? 128
+                              : NEED <= 256 ? 256 : 512;
+};
+
+template <bool TS, int M, int N>
+__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, long long* cycles) {
+  using P = ProbeCfg<TS, M, N>;
+  extern __shared__ __align__(1024) uint8_t probe_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(probe_raw) + 1023) &
+                                           ~uintptr_t(1023));
+  uint8_t* a_s = sm;
+  uint8_t* b_s = sm + P::A_BYTES;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(b_s + P::B_BYTES);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(slot, P::COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t base = *slot;
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = idesc_f16(M, N, 0);
+    const uint64_t adesc = smem_desc(smem_u32(a_s), 16, 1024, 2);
+    const uint64_t bdesc = smem_desc(smem_u32(b_s), 16, 1024, 2);
+    const long long t0 = clock64();
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        if constexpr (TS)
+          umma_f16_ts(base, base + N + kk * 8, bdesc + (uint64_t)((kk * 32) >> 4), idesc, 1u);
+        else
+          umma_f16_ss(base, adesc + (uint64_t)((kk * 32) >> 4),
+                      bdesc + (uint64_t)((kk * 32) >> 4), idesc, 1u);
+      }
+    }
+    umma_commit(bar);
+    mbar_wait(bar, 0, nullptr, 0);
+    cycles[blockIdx.x] = clock64() - t0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(base, P::COLS);
+}
+
+template <bool TS, int M, int N>
+static int probe_t(int iters, int ctas, long long* cycles, cudaStream_t s) {
+  using P = ProbeCfg<TS, M, N>;
+  static unsigned long long done = 0;
+  if (!smem_attr_once(mma_probe_kernel<TS, M, N>, P::SMEM, &done)) return -3;
+  mma_probe_kernel<TS, M, N><<<ctas, 128, P::SMEM, s>>>(iters, cycles);
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
+}
+
+}  // namespace swarm
+
+using namespace swarm;
+
+// Shapes, by index: the (TS?, M, N) of mma_probe_shape().
+static const int kProbeShapes[][3] = {
+    {1, 128, 16}, {1, 128, 32}, {1, 128, 64}, {1, 128, 128}, {1, 128, 256},
+    {0, 128, 32}, {0, 128, 128}, {0, 128, 256}, {0, 64, 64}, {0, 64, 128}, {0, 64, 256}};
+
+int mma_probe_shapes() { return (int)(sizeof(kProbeShapes) / sizeof(kProbeShapes[0])); }
+
+void mma_probe_shape(int i, int* ts, int* m, int* n) {
+  *ts = kProbeShapes[i][0];
+  *m = kProbeShapes[i][1];
+  *n = kProbeShapes[i][2];
+}
+
+int launch_mma_probe(int shape, int iters, int ctas, long long* cycles, cudaStream_t s) {
+  switch (shape) {
+    case 0: return probe_t<true, 128, 16>(iters, ctas, cycles, s);
+    case 1: return probe_t<true, 128, 32>(iters, ctas, cycles, s);
+    case 2: return probe_t<true, 128, 64>(iters, ctas, cycles, s);
+    case 3: return probe_t<true, 128, 128>(iters, ctas, cycles, s);
+    case 4: return probe_t<true, 128, 256>(iters, ctas, cycles, s);
+    case 5: return probe_t<false, 128, 32>(iters, ctas, cycles, s);
+    case 6: return probe_t<false, 128, 128>(iters, ctas, cycles, s);
+    case 7: return probe_t<false, 128, 256>(iters, ctas, cycles, s);
+    case 8: return probe_t<false, 64, 64>(iters, ctas, cycles, s);
+    case 9: return probe_t<false, 64, 128>(iters, ctas, cycles, s);
+    case 10: return probe_t<false, 64, 256>(iters, ctas, cycles, s);
+    default: return -1;
+  }
+}

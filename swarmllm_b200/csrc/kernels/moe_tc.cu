@@ -518,6 +518,7 @@ __global__ void __launch_bounds__(512) moe_combine_kernel(
     GemmOut sh, int has_sh, GemmOut shg, int has_shg, float* __restrict__ residual, int H,
     const float* __restrict__ norm_w, __half* __restrict__ out, int out_stride, float eps) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   extern __shared__ float crow[];
   __shared__ float red[32];
   const int t = blockIdx.x;
@@ -790,6 +791,7 @@ __global__ void __launch_bounds__(256) moe_combine_cluster_kernel(
     GemmOut sh, int has_sh, GemmOut shg, int has_shg, float* __restrict__ residual, int H,
     const float* __restrict__ norm_w, __half* __restrict__ out, int out_stride, float eps) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float part;
   __shared__ float red[32];

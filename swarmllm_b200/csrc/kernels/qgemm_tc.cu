@@ -194,6 +194,8 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
   const long u0 = (long)blockIdx.x * a.upc;
   const long u1 = min(a.total_units, u0 + a.upc);
   const int n_units = (int)max(0L, u1 - u0);
+  // the next kernel (an epilogue) may launch now; it waits for this grid
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::W_ST; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], 4); }

@@ -126,6 +126,7 @@ __global__ void __launch_bounds__(kGvWarps * 32)
   const long u0 = (long)blockIdx.x * a.upc;
   const long u1 = min(a.total_units, u0 + a.upc);
   const int n = (int)max(0L, u1 - u0);
+  pdl_trigger();   // the next kernel (an epilogue) may launch now; it waits for this grid
 
   if (lane == 0) {
     for (int s = 0; s < kGvWStages + kGvXStages; ++s) mbar_init(&wfull[s], 1);

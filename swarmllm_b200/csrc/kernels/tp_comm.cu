@@ -101,6 +101,7 @@ SW_DEVICE float4 add4(float4 a, float4 b) {
 // the rank's own columns of the slice, phase 3 (normalise) 1/C of the whole row.
 __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const TpReduceArgs a) {
   pdl_trigger();  // dependents (the next GEMM) may launch and prefetch weights
+  pdl_wait();     // what earlier kernels wrote is complete and visible
   __shared__ float red[32];
   __shared__ int ok_s;
   const int H = a.H, W = a.W, C = a.C;
@@ -234,6 +235,7 @@ struct TpLocalArgs {
 
 __global__ void __launch_bounds__(256) tp_local_norm_kernel(const TpLocalArgs a) {
   pdl_trigger();
+  pdl_wait();
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float part;
   __shared__ float red[32];
@@ -336,23 +338,13 @@ int launch_tp_local_norm(const GemmOut& g, float* residual, const float* bias, c
   a.code = code;
   a.timeout_ns = timeout_ns > 0 ? (unsigned long long)timeout_ns : tc::kWaitTimeoutNs;
   const int per = dim / kTpCluster;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(g.T * kTpCluster);
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = (size_t)per * sizeof(float);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kTpCluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   if ((size_t)per * sizeof(float) > 48 * 1024 &&
       cudaFuncSetAttribute(tp_local_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)(per * sizeof(float))) != cudaSuccess)
     return -4;
-  if (cudaLaunchKernelEx(&cfg, tp_local_norm_kernel, a) != cudaSuccess) return -4;
+  if (launch_pdl_cluster(tp_local_norm_kernel, dim3(g.T * kTpCluster), dim3(256),
+                         (size_t)per * sizeof(float), s, kTpCluster, a) != cudaSuccess)
+    return -4;
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -403,6 +395,6 @@ int launch_tp_reduce_norm(const GemmOut& g, const float* bias, const float* w, _
   // at most 2 CTAs per SM: every CTA resident, rows in ascending order on every rank
   const int units = T * C;
   const int grid = units < 2 * num_sms ? units : 2 * num_sms;
-  tp_reduce_norm_kernel<<<grid, 256, 0, s>>>(a);
+  launch_pdl(tp_reduce_norm_kernel, dim3(grid), dim3(256), 0, s, a);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }

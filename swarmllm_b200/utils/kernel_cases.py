@@ -1,8 +1,8 @@
 """Standalone cases of the hot kernels, for profiling one kernel at a time:
 
     python -m swarmllm_b200.utils.kernel_cases \
-        {qgemm|qgemm_sweep|qgemv|qgemv_o|dense|attn|attn_prefill|rmsnorm|swiglu|rope_kv|moe|delta|
-         delta_decode|tree_rank|sample} [--time] [--qtype Q4_K|Q6_K|Q8_0]
+        {qgemm|qgemm_sweep|mma_probe|qgemv|qgemv_o|dense|attn|attn_prefill|rmsnorm|swiglu|
+         rope_kv|moe|delta|delta_decode|tree_rank|sample} [--time] [--qtype Q4_K|Q6_K|Q8_0]
 
 Each case builds benchmark-sized operands on cuda:0 (inputs larger than the
 126 MB L2 where memory traffic matters; tree_rank and sample use the real
@@ -70,6 +70,22 @@ def run_case(which: str, TIME: bool = False, qtype: str = "Q4_K") -> None:
                       f"{rows * K * bb / bv / us / 1e3:6.0f} GB/s"
                       f"  {2 * rows * K * T / us / 1e6:7.1f} TFLOP/s", flush=True)
                 ws.check()
+    elif which == "mma_probe":   # tcgen05.mma issue cost per shape (one CTA per SM, clock64)
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+        iters = 2048
+        for i, (ts, m, n) in enumerate(C().mma_probe_shapes()):
+            cyc = torch.zeros(sms, dtype=torch.int64, device=dev)
+            C().mma_probe(i, 64, cyc)                  # warm-up
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            C().mma_probe(i, iters, cyc)
+            b.record()
+            torch.cuda.synchronize()
+            per = float(cyc.float().median()) / (iters * 4)
+            ns = a.elapsed_time(b) * 1e6 / (iters * 4)
+            flop = 2.0 * m * n * 16 * sms / (ns * 1e-9) / 1e12
+            print(f"{'TS' if ts else 'SS'} M={m:3d} N={n:3d} K=16: {per:6.1f} clk/MMA  "
+                  f"{ns:6.1f} ns/MMA  {flop:7.1f} TFLOP/s (all SMs)", flush=True)
     elif which == "qgemm":       # Llama-3.3-70B gate|up at decode batch 32 (264 MB of weights)
         from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
         rows, K, T = 57344, 8192, 32
