@@ -3,8 +3,11 @@
 // One CTA per SM issues `iters` x 4 MMAs of one shape (M x N x 16, fp16 in,
 // fp32 accumulate) back to back from one thread, commits once and waits; the
 // clock64 difference per MMA is what a weight-streaming GEMM pays per
-// instruction.  Operands are whatever shared memory / TMEM holds (the values
-// do not matter), laid out as the GEMMs lay theirs out: K-major, 128-byte
+// instruction.  With `group` > 0 the thread commits and waits for completion
+// after every `group` MMAs instead: the round trip a pipeline pays when it
+// has to see MMAs finish before it can refill their operands.  Operands are
+// whatever shared memory / TMEM holds (the values do not matter), laid out
+// as the GEMMs lay theirs out: K-major, 128-byte
 // swizzle, 8-row groups of 1024 bytes, four K = 16 steps inside one 128-byte
 // row.  TS = A from TMEM (the quantized GEMM's form), SS = A from shared memory.
 #include "kernels.h"
@@ -26,7 +29,8 @@ struct ProbeCfg {
 };
 
 template <bool TS, int M, int N>
-__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, long long* cycles) {
+__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, int group,
+                                                           long long* cycles) {
   using P = ProbeCfg<TS, M, N>;
   extern __shared__ __align__(1024) uint8_t probe_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(probe_raw) + 1023) &
@@ -53,6 +57,8 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, long long*
     const uint64_t adesc = smem_desc(smem_u32(a_s), 16, 1024, 2);
     const uint64_t bdesc = smem_desc(smem_u32(b_s), 16, 1024, 2);
     const long long t0 = clock64();
+    uint32_t phase = 0;
+    int issued = 0;
     for (int it = 0; it < iters; ++it) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
@@ -62,9 +68,15 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, long long*
           umma_f16_ss(base, adesc + (uint64_t)((kk * 32) >> 4),
                       bdesc + (uint64_t)((kk * 32) >> 4), idesc, 1u);
       }
+      issued += 4;
+      if (group > 0 && issued % group == 0) {
+        umma_commit(bar);
+        if (!mbar_wait(bar, phase, nullptr, 0)) break;
+        phase ^= 1;
+      }
     }
     umma_commit(bar);
-    mbar_wait(bar, 0, nullptr, 0);
+    mbar_wait(bar, phase, nullptr, 0);
     cycles[blockIdx.x] = clock64() - t0;
   }
   tc_fence_before();
@@ -74,11 +86,11 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, long long*
 }
 
 template <bool TS, int M, int N>
-static int probe_t(int iters, int ctas, long long* cycles, cudaStream_t s) {
+static int probe_t(int iters, int group, int ctas, long long* cycles, cudaStream_t s) {
   using P = ProbeCfg<TS, M, N>;
   static unsigned long long done = 0;
   if (!smem_attr_once(mma_probe_kernel<TS, M, N>, P::SMEM, &done)) return -3;
-  mma_probe_kernel<TS, M, N><<<ctas, 128, P::SMEM, s>>>(iters, cycles);
+  mma_probe_kernel<TS, M, N><<<ctas, 128, P::SMEM, s>>>(iters, group, cycles);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -99,19 +111,21 @@ void mma_probe_shape(int i, int* ts, int* m, int* n) {
   *n = kProbeShapes[i][2];
 }
 
-int launch_mma_probe(int shape, int iters, int ctas, long long* cycles, cudaStream_t s) {
+int launch_mma_probe(int shape, int iters, int group, int ctas, long long* cycles,
+                     cudaStream_t s) {
+  if (group < 0 || group % 4) return -1;
   switch (shape) {
-    case 0: return probe_t<true, 128, 16>(iters, ctas, cycles, s);
-    case 1: return probe_t<true, 128, 32>(iters, ctas, cycles, s);
-    case 2: return probe_t<true, 128, 64>(iters, ctas, cycles, s);
-    case 3: return probe_t<true, 128, 128>(iters, ctas, cycles, s);
-    case 4: return probe_t<true, 128, 256>(iters, ctas, cycles, s);
-    case 5: return probe_t<false, 128, 32>(iters, ctas, cycles, s);
-    case 6: return probe_t<false, 128, 128>(iters, ctas, cycles, s);
-    case 7: return probe_t<false, 128, 256>(iters, ctas, cycles, s);
-    case 8: return probe_t<false, 64, 64>(iters, ctas, cycles, s);
-    case 9: return probe_t<false, 64, 128>(iters, ctas, cycles, s);
-    case 10: return probe_t<false, 64, 256>(iters, ctas, cycles, s);
+    case 0: return probe_t<true, 128, 16>(iters, group, ctas, cycles, s);
+    case 1: return probe_t<true, 128, 32>(iters, group, ctas, cycles, s);
+    case 2: return probe_t<true, 128, 64>(iters, group, ctas, cycles, s);
+    case 3: return probe_t<true, 128, 128>(iters, group, ctas, cycles, s);
+    case 4: return probe_t<true, 128, 256>(iters, group, ctas, cycles, s);
+    case 5: return probe_t<false, 128, 32>(iters, group, ctas, cycles, s);
+    case 6: return probe_t<false, 128, 128>(iters, group, ctas, cycles, s);
+    case 7: return probe_t<false, 128, 256>(iters, group, ctas, cycles, s);
+    case 8: return probe_t<false, 64, 64>(iters, group, ctas, cycles, s);
+    case 9: return probe_t<false, 64, 128>(iters, group, ctas, cycles, s);
+    case 10: return probe_t<false, 64, 256>(iters, group, ctas, cycles, s);
     default: return -1;
   }
 }

@@ -108,10 +108,11 @@ SW_DEVICE void q4k_scales_h2(const uint4& hdr, __half2 (&S)[4], __half2 (&NM)[4]
   }
 }
 
-// Sub-blocks [4h, 4h+4) of one row's superblock (K 128h .. 128h+127) into 64
-// TMEM columns at taddr + 64h, from the fp16 scale pairs of q4k_scales_h2.
+// Sub-blocks [4h, 4h+4) of one row's superblock (K 128h .. 128h+127) as the
+// 64 32-bit TMEM columns [64h, 64h + 64) of the unit, in registers, from the
+// fp16 scale pairs of q4k_scales_h2.
 SW_DEVICE void dq_half_h2(const uint4 (&q)[8], const __half2 (&S)[4], const __half2 (&NM)[4],
-                          uint32_t taddr, int h) {
+                          int h, uint32_t (&out)[64]) {
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
   const __half2 SIXTEENTH = u32_as_h2(0x2C002C00u);
 #pragma unroll
@@ -121,11 +122,15 @@ SW_DEVICE void dq_half_h2(const uint4 (&q)[8], const __half2 (&S)[4], const __ha
     const __half2 Sj = (sub & 1) ? __high2half2(Sp) : __low2half2(Sp);
     const __half2 MB = (sub & 1) ? __high2half2(Mp) : __low2half2(Mp);
     const __half2 S16 = __hmul2(Sj, SIXTEENTH);
-    uint32_t cols[16];
 #pragma unroll
-    for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[4 * sub + w4], Sj, S16, MB, cols + 4 * w4);
-    tmem_st_x16(taddr + sub * 16, cols);
+    for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[4 * sub + w4], Sj, S16, MB, out + 16 * k + 4 * w4);
   }
+}
+
+// The 64 columns of half h from registers into TMEM (taddr: the unit's column 0).
+SW_DEVICE void store_half(uint32_t taddr, int h, const uint32_t (&cols)[64]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) tmem_st_x16(taddr + 64 * h + 16 * k, cols + 16 * k);
 }
 
 // Dequantize one row's superblock (256 K values) into the unit's 128 TMEM columns.

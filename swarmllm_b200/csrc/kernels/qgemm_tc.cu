@@ -59,15 +59,16 @@ struct QCfg {
   static constexpr int DQ = N <= 64 ? 3 : 2;
   static constexpr int U = DQ;                           // unit stages in flight
   // Hand-offs per unit between the dequantizers and the MMA issuer: 2 = per
-  // K half (64 columns), so the first half's MMAs overlap the second half's
-  // dequantization; 1 = whole units (fewer barrier round trips).
+  // K half (64 columns), each dequantized into registers before its TMEM
+  // half is free, so the first half's MMAs overlap the second half's
+  // dequantization; 1 = whole units, dequantized after the wait.
 // Timing experiments only (results are wrong): 1 = dequantizers skip the
 // TMEM writes, 2 = the MMA issuer skips the MMAs (commits still flow).
 #ifndef SWARMLLM_QGEMM_EXPERIMENT
 #define SWARMLLM_QGEMM_EXPERIMENT 0
 #endif
 #ifndef SWARMLLM_QGEMM_HALVES
-#define SWARMLLM_QGEMM_HALVES 1
+#define SWARMLLM_QGEMM_HALVES 2
 #endif
   static constexpr int HALVES = SWARMLLM_QGEMM_HALVES;
   static constexpr int THREADS = 96 + 128 * DQ;          // W producer, MMA, X producer, DQ WGs
@@ -141,7 +142,10 @@ struct QGemmArgs {
 
 // One dequantizer warp's part of a unit: stage -> registers (freeing the
 // stage), then the unit's TMEM A stage in H hand-offs (H = 2: one per K half
-// of 64 columns), each once the MMAs that last read that part have completed.
+// of 64 columns).  With H = 2 each half is dequantized into registers BEFORE
+// waiting for the MMAs that last read that half of the stage, so the wait is
+// followed only by the TMEM stores: the stage turns around in the time of the
+// stores, not of the dequantization.
 template <class F, int H>
 SW_DEVICE bool dq_unit_fmt(const uint8_t* stage, int row, uint64_t* w_empty, uint64_t* empty_h,
                            uint64_t* ready_h, uint32_t empty_parity, uint32_t taddr, int* status,
@@ -153,11 +157,20 @@ SW_DEVICE bool dq_unit_fmt(const uint8_t* stage, int row, uint64_t* w_empty, uin
   F::prep(r);
 #pragma unroll
   for (int h = 0; h < H; ++h) {
+    uint32_t cols[64];
+    if (H == 2) F::dq_half(r, h, cols);
     if (!mbar_wait_warp(&empty_h[h], empty_parity, status, 32, i, h)) return false;
     tc_fence_after();
 #if SWARMLLM_QGEMM_EXPERIMENT != 1
+    if (H == 2) {
+      store_half(taddr, h, cols);
+    } else {
 #pragma unroll
-    for (int q = 0; q < 2 / H; ++q) F::dq_half(r, taddr, h * (2 / H) + q);
+      for (int q = 0; q < 2; ++q) {
+        F::dq_half(r, q, cols);
+        store_half(taddr, q, cols);
+      }
+    }
 #endif
     tmem_wait_st();
     tc_fence_before();

@@ -86,6 +86,17 @@ def run_case(which: str, TIME: bool = False, qtype: str = "Q4_K") -> None:
             flop = 2.0 * m * n * 16 * sms / (ns * 1e-9) / 1e12
             print(f"{'TS' if ts else 'SS'} M={m:3d} N={n:3d} K=16: {per:6.1f} clk/MMA  "
                   f"{ns:6.1f} ns/MMA  {flop:7.1f} TFLOP/s (all SMs)", flush=True)
+        # the round trip of a refill: commit + wait after every 16 MMAs (one 256-K unit)
+        for i, (ts, m, n) in enumerate(C().mma_probe_shapes()):
+            if not ts or n > 64:
+                continue
+            for grp in (4, 16, 48):
+                cyc = torch.zeros(sms, dtype=torch.int64, device=dev)
+                C().mma_probe(i, 512, cyc, grp)
+                torch.cuda.synchronize()
+                per = float(cyc.float().median()) / (512 * 4)
+                print(f"TS M={m:3d} N={n:3d}, commit+wait every {grp:2d} MMAs: {per:6.1f} clk/MMA "
+                      f"({per * grp:7.1f} clk per group)", flush=True)
     elif which == "qgemm":       # Llama-3.3-70B gate|up at decode batch 32 (264 MB of weights)
         from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
         rows, K, T = 57344, 8192, 32
