@@ -517,13 +517,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     }
     return v;
   });
-  m.def("mma_probe", [](int64_t shape, int64_t iters, Tensor cycles, int64_t group) {
+  m.def("mma_probe", [](int64_t shape, int64_t iters, Tensor cycles, int64_t group, int64_t mode,
+                        int64_t spin) {
     CHECK_DT(cycles, at::kLong);
     const at::cuda::CUDAGuard guard(cycles.device());
-    TORCH_CHECK(launch_mma_probe((int)shape, (int)iters, (int)group, (int)cycles.numel(),
+    TORCH_CHECK(launch_mma_probe((int)shape, (int)iters, (int)group, (int)mode, (int)spin,
+                                 (int)cycles.numel(),
                                  reinterpret_cast<long long*>(cycles.data_ptr<int64_t>()),
                                  cur_stream()) == 0, "mma_probe launch failed");
-  }, py::arg("shape"), py::arg("iters"), py::arg("cycles"), py::arg("group") = 0);
+  }, py::arg("shape"), py::arg("iters"), py::arg("cycles"), py::arg("group") = 0,
+     py::arg("mode") = 1, py::arg("spin") = 0);
   // Bounded wait for `world` epoch flags (flags: device address of uint32[world]);
   // timeout_ns <= 0 uses the kernels' default deadline (1 s).
   m.def("flag_wait", [](int64_t flags, int64_t world, Tensor ctl, int64_t slot, Tensor status,

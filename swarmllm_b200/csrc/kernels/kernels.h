@@ -209,12 +209,13 @@ int launch_tp_local_norm(const swarm::GemmOut& g, float* residual, const float* 
                          int code, long long timeout_ns, cudaStream_t s);
 
 // Diagnostics (mma_probe.cu): clock64 cycles of `iters` x 4 back-to-back
-// tcgen05.mma of probe shape `shape` (commit + wait every `group` MMAs when
-// group > 0), one entry per CTA.
+// tcgen05.mma of probe shape `shape` (every `group` MMAs, when group > 0: a
+// commit, with a wait if mode & 1, or a `spin`-clock pause if mode & 4; mode
+// & 2 rotates over 4 accumulators), one entry per CTA.
 int mma_probe_shapes();
 void mma_probe_shape(int i, int* ts, int* m, int* n);
-int launch_mma_probe(int shape, int iters, int group, int ctas, long long* cycles,
-                     cudaStream_t s);
+int launch_mma_probe(int shape, int iters, int group, int mode, int spin, int ctas,
+                     long long* cycles, cudaStream_t s);
 
 // GGML blocks -> fp16 [rows][K] (qmatmul_simt.cu); quantized types only.
 int launch_dequant_f16(const void* w, int type, int rows, int K, __half* out, cudaStream_t s);

@@ -3,9 +3,11 @@
 // One CTA per SM issues `iters` x 4 MMAs of one shape (M x N x 16, fp16 in,
 // fp32 accumulate) back to back from one thread, commits once and waits; the
 // clock64 difference per MMA is what a weight-streaming GEMM pays per
-// instruction.  With `group` > 0 the thread commits and waits for completion
-// after every `group` MMAs instead: the round trip a pipeline pays when it
-// has to see MMAs finish before it can refill their operands.  Operands are
+// instruction.  With `group` > 0 the thread commits after every `group` MMAs
+// (mode bit 0: and waits for completion -- the round trip a pipeline pays when
+// it has to see MMAs finish before it can refill their operands; bit 1: the
+// MMAs rotate over 4 accumulators; bit 2: instead of committing, the thread
+// spins `spin` clocks, idling the issue like a wait would).  Operands are
 // whatever shared memory / TMEM holds (the values do not matter), laid out
 // as the GEMMs lay theirs out: K-major, 128-byte
 // swizzle, 8-row groups of 1024 bytes, four K = 16 steps inside one 128-byte
@@ -23,14 +25,16 @@ struct ProbeCfg {
   static constexpr int A_BYTES = TS ? 0 : M * 128;
   static constexpr int B_BYTES = N * 128;
   static constexpr int SMEM = 1024 + A_BYTES + B_BYTES + 64;
-  static constexpr int NEED = N + (TS ? 32 : 0);   // D columns (+ A for TS)
+  // D accumulators (4 for the rotating mode, which needs 4N + 32 <= 512) + A for TS
+  static constexpr bool ROT_OK = 4 * N + 32 <= 512;
+  static constexpr int NEED = (ROT_OK ? 4 * N : N) + (TS ? 32 : 0);
   static constexpr int COLS = NEED <= 32 ? 32 : NEED <= 64 ? 64 : NEED <= 128 ? 128
                               : NEED <= 256 ? 256 : 512;
 };
 
 template <bool TS, int M, int N>
-__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, int group,
-                                                           long long* cycles) {
+__global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, int group, int mode,
+                                                           int spin, long long* cycles) {
   using P = ProbeCfg<TS, M, N>;
   extern __shared__ __align__(1024) uint8_t probe_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(probe_raw) + 1023) &
@@ -59,21 +63,37 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, int group,
     const long long t0 = clock64();
     uint32_t phase = 0;
     int issued = 0;
+    const bool rotate = P::ROT_OK && (mode & 2) != 0;
+    const uint32_t a_col = (uint32_t)((P::ROT_OK ? 4 : 1) * N);   // A (TS) after the D columns
     for (int it = 0; it < iters; ++it) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t d = base + (rotate ? (uint32_t)(kk * N) : 0u);
         if constexpr (TS)
-          umma_f16_ts(base, base + N + kk * 8, bdesc + (uint64_t)((kk * 32) >> 4), idesc, 1u);
+          umma_f16_ts(d, base + a_col + kk * 8, bdesc + (uint64_t)((kk * 32) >> 4), idesc, 1u);
         else
-          umma_f16_ss(base, adesc + (uint64_t)((kk * 32) >> 4),
+          umma_f16_ss(d, adesc + (uint64_t)((kk * 32) >> 4),
                       bdesc + (uint64_t)((kk * 32) >> 4), idesc, 1u);
       }
       issued += 4;
       if (group > 0 && issued % group == 0) {
-        umma_commit(bar);
-        if (!mbar_wait(bar, phase, nullptr, 0)) break;
-        phase ^= 1;
+        if (mode & 4) {
+          const long long ts = clock64();
+          while (clock64() - ts < spin) {
+          }
+        } else {
+          umma_commit(bar);
+          if (mode & 1) {
+            if (!mbar_wait(bar, phase, nullptr, 0)) break;
+            phase ^= 1;
+          }
+        }
       }
+    }
+    if (group > 0 && !(mode & 1) && !(mode & 4)) {
+      // commits without waits: their arrivals completed phases in passing;
+      // count them to know the parity of the final one
+      phase = (uint32_t)((issued / group) & 1);
     }
     umma_commit(bar);
     mbar_wait(bar, phase, nullptr, 0);
@@ -86,11 +106,14 @@ __global__ void __launch_bounds__(128, 1) mma_probe_kernel(int iters, int group,
 }
 
 template <bool TS, int M, int N>
-static int probe_t(int iters, int group, int ctas, long long* cycles, cudaStream_t s) {
+static int probe_t(int iters, int group, int mode, int spin, int ctas, long long* cycles,
+                   cudaStream_t s) {
   using P = ProbeCfg<TS, M, N>;
+  static_assert(P::NEED <= 512, "TMEM columns");
+  if ((mode & 2) && !P::ROT_OK) return -1;
   static unsigned long long done = 0;
   if (!smem_attr_once(mma_probe_kernel<TS, M, N>, P::SMEM, &done)) return -3;
-  mma_probe_kernel<TS, M, N><<<ctas, 128, P::SMEM, s>>>(iters, group, cycles);
+  mma_probe_kernel<TS, M, N><<<ctas, 128, P::SMEM, s>>>(iters, group, mode, spin, cycles);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
@@ -111,21 +134,21 @@ void mma_probe_shape(int i, int* ts, int* m, int* n) {
   *n = kProbeShapes[i][2];
 }
 
-int launch_mma_probe(int shape, int iters, int group, int ctas, long long* cycles,
-                     cudaStream_t s) {
+int launch_mma_probe(int shape, int iters, int group, int mode, int spin, int ctas,
+                     long long* cycles, cudaStream_t s) {
   if (group < 0 || group % 4) return -1;
   switch (shape) {
-    case 0: return probe_t<true, 128, 16>(iters, group, ctas, cycles, s);
-    case 1: return probe_t<true, 128, 32>(iters, group, ctas, cycles, s);
-    case 2: return probe_t<true, 128, 64>(iters, group, ctas, cycles, s);
-    case 3: return probe_t<true, 128, 128>(iters, group, ctas, cycles, s);
-    case 4: return probe_t<true, 128, 256>(iters, group, ctas, cycles, s);
-    case 5: return probe_t<false, 128, 32>(iters, group, ctas, cycles, s);
-    case 6: return probe_t<false, 128, 128>(iters, group, ctas, cycles, s);
-    case 7: return probe_t<false, 128, 256>(iters, group, ctas, cycles, s);
-    case 8: return probe_t<false, 64, 64>(iters, group, ctas, cycles, s);
-    case 9: return probe_t<false, 64, 128>(iters, group, ctas, cycles, s);
-    case 10: return probe_t<false, 64, 256>(iters, group, ctas, cycles, s);
+    case 0: return probe_t<true, 128, 16>(iters, group, mode, spin, ctas, cycles, s);
+    case 1: return probe_t<true, 128, 32>(iters, group, mode, spin, ctas, cycles, s);
+    case 2: return probe_t<true, 128, 64>(iters, group, mode, spin, ctas, cycles, s);
+    case 3: return probe_t<true, 128, 128>(iters, group, mode, spin, ctas, cycles, s);
+    case 4: return probe_t<true, 128, 256>(iters, group, mode, spin, ctas, cycles, s);
+    case 5: return probe_t<false, 128, 32>(iters, group, mode, spin, ctas, cycles, s);
+    case 6: return probe_t<false, 128, 128>(iters, group, mode, spin, ctas, cycles, s);
+    case 7: return probe_t<false, 128, 256>(iters, group, mode, spin, ctas, cycles, s);
+    case 8: return probe_t<false, 64, 64>(iters, group, mode, spin, ctas, cycles, s);
+    case 9: return probe_t<false, 64, 128>(iters, group, mode, spin, ctas, cycles, s);
+    case 10: return probe_t<false, 64, 256>(iters, group, mode, spin, ctas, cycles, s);
     default: return -1;
   }
 }

@@ -7,10 +7,10 @@
 // and partial-slot format do not depend on the format.  A format supplies:
 //   Regs           one weight row's share of a unit, in registers
 //   load / prep    shared memory -> registers; scale decode (before any wait)
-//   dq_half(h)     K [128h, 128h+128) -> the 64 TMEM columns of that half as
+//   dq_chunk(c)    K [32c, 32c+32) -> the 16 TMEM columns [16c, 16c+16) as
 //                  fp16 pairs, in registers (A operand of tcgen05.mma, lane =
 //                  row, 32-bit column c = K values 2c, 2c+1); the GEMM stores
-//                  them into TMEM with store_half
+//                  them into TMEM
 //   gemv_prep,     acc[t] += sum_k W[row][k] * X[t][k] on the CUDA cores
 //   gemv<T>
 //
@@ -59,8 +59,8 @@ struct FmtQ4K {
     r.hdr = src[8];
   }
   static SW_DEVICE void prep(Regs& r) { q4k_scales_h2(r.hdr, r.S, r.NM); }
-  static SW_DEVICE void dq_half(const Regs& r, int h, uint32_t (&out)[64]) {
-    dq_half_h2(r.q, r.S, r.NM, h, out);
+  static SW_DEVICE void dq_chunk(const Regs& r, int c, uint32_t (&out)[16]) {
+    dq_chunk_h2(r.q, r.S, r.NM, c, out);
   }
   static SW_DEVICE void gemv_prep(Regs& r) { q4k_scales_f32(r.hdr, r.sc, r.mb); }
 
@@ -244,14 +244,11 @@ struct FmtQ6K {
   }
   static SW_DEVICE void prep(Regs&) {}
   static SW_DEVICE void gemv_prep(Regs&) {}
-  static SW_DEVICE void dq_half(const Regs& r, int h, uint32_t (&out)[64]) {
+  static SW_DEVICE void dq_chunk(const Regs& r, int sp, uint32_t (&cols)[16]) {
     const uint32_t* lw = reinterpret_cast<const uint32_t*>(r.lo);
     const uint32_t* hw = reinterpret_cast<const uint32_t*>(r.hc);
     const uint32_t* sw = reinterpret_cast<const uint32_t*>(r.sc);   // scale pairs (2s, 2s+1)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {             // two sub-blocks = 32 K = 16 columns
-      const int sp = 4 * h + k;
-      uint32_t* cols = out + 16 * k;
+    {                                         // two sub-blocks = 32 K = 16 columns
       const __half2 s2 = u32_as_h2(sw[sp]);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -330,17 +327,13 @@ struct FmtQ80 {
   }
   static SW_DEVICE void prep(Regs&) {}
   static SW_DEVICE void gemv_prep(Regs&) {}
-  static SW_DEVICE void dq_half(const Regs& r, int h, uint32_t (&out)[64]) {
+  static SW_DEVICE void dq_chunk(const Regs& r, int b, uint32_t (&out)[16]) {
     const uint32_t* qw = reinterpret_cast<const uint32_t*>(r.q);
     const uint32_t* dw = reinterpret_cast<const uint32_t*>(&r.d);
+    const __half2 d2 = u32_as_h2(dw[b >> 1]);   // one 32-value block = 16 columns
+    const __half2 D = (b & 1) ? __high2half2(d2) : __low2half2(d2);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {             // one 32-value block = 16 columns
-      const int b = 4 * h + k;
-      const __half2 d2 = u32_as_h2(dw[b >> 1]);
-      const __half2 D = (b & 1) ? __high2half2(d2) : __low2half2(d2);
-#pragma unroll
-      for (int w = 0; w < 8; ++w) q80_word(qw[8 * b + w], D, out + 16 * k + 2 * w);
-    }
+    for (int w = 0; w < 8; ++w) q80_word(qw[8 * b + w], D, out + 2 * w);
   }
   // Weights are scaled before the products (q*d is what the tensor-core path
   // multiplies too), so the fp16 partials hold ordinary w*x sums.

@@ -108,29 +108,44 @@ SW_DEVICE void q4k_scales_h2(const uint4& hdr, __half2 (&S)[4], __half2 (&NM)[4]
   }
 }
 
-// Sub-blocks [4h, 4h+4) of one row's superblock (K 128h .. 128h+127) as the
-// 64 32-bit TMEM columns [64h, 64h + 64) of the unit, in registers, from the
-// fp16 scale pairs of q4k_scales_h2.
-SW_DEVICE void dq_half_h2(const uint4 (&q)[8], const __half2 (&S)[4], const __half2 (&NM)[4],
-                          int h, uint32_t (&out)[64]) {
+// Sub-block c (K 32c .. 32c+31) of one row's superblock as the 16 32-bit
+// TMEM columns [16c, 16c + 16) of the unit, in registers, from the fp16
+// scale pairs of q4k_scales_h2.
+SW_DEVICE void dq_chunk_h2(const uint4 (&q)[8], const __half2 (&S)[4], const __half2 (&NM)[4],
+                           int c, uint32_t (&out)[16]) {
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(q);
   const __half2 SIXTEENTH = u32_as_h2(0x2C002C00u);
+  const __half2 Sp = S[c >> 1], Mp = NM[c >> 1];
+  const __half2 Sj = (c & 1) ? __high2half2(Sp) : __low2half2(Sp);
+  const __half2 MB = (c & 1) ? __high2half2(Mp) : __low2half2(Mp);
+  const __half2 S16 = __hmul2(Sj, SIXTEENTH);
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int sub = 4 * h + k;
-    const __half2 Sp = S[sub >> 1], Mp = NM[sub >> 1];
-    const __half2 Sj = (sub & 1) ? __high2half2(Sp) : __low2half2(Sp);
-    const __half2 MB = (sub & 1) ? __high2half2(Mp) : __low2half2(Mp);
-    const __half2 S16 = __hmul2(Sj, SIXTEENTH);
-#pragma unroll
-    for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[4 * sub + w4], Sj, S16, MB, out + 16 * k + 4 * w4);
-  }
+  for (int w4 = 0; w4 < 4; ++w4) dq_word(qw[4 * c + w4], Sj, S16, MB, out + 4 * w4);
 }
 
 // The 64 columns of half h from registers into TMEM (taddr: the unit's column 0).
 SW_DEVICE void store_half(uint32_t taddr, int h, const uint32_t (&cols)[64]) {
 #pragma unroll
   for (int k = 0; k < 4; ++k) tmem_st_x16(taddr + 64 * h + 16 * k, cols + 16 * k);
+}
+
+// Half h (chunks 4h .. 4h+3) of a format into registers.
+template <class F>
+SW_DEVICE void dq_half_regs(const typename F::Regs& r, int h, uint32_t (&out)[64]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    F::dq_chunk(r, 4 * h + k, *reinterpret_cast<uint32_t(*)[16]>(out + 16 * k));
+}
+
+// A whole unit, chunk by chunk, straight into TMEM (16 registers live at a time).
+template <class F>
+SW_DEVICE void dq_unit_store(const typename F::Regs& r, uint32_t taddr) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t cols[16];
+    F::dq_chunk(r, c, cols);
+    tmem_st_x16(taddr + 16 * c, cols);
+  }
 }
 
 // Dequantize one row's superblock (256 K values) into the unit's 128 TMEM columns.

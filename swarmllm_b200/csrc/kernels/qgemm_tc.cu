@@ -68,7 +68,12 @@ struct QCfg {
 #define SWARMLLM_QGEMM_EXPERIMENT 0
 #endif
 #ifndef SWARMLLM_QGEMM_HALVES
-#define SWARMLLM_QGEMM_HALVES 2
+#define SWARMLLM_QGEMM_HALVES 1
+#endif
+// Activation ring depth: 0 = tied to the TMEM A stages (one MMA commit per
+// unit releases both), else the deepest ring that fits (its own commit).
+#ifndef SWARMLLM_QGEMM_XRING
+#define SWARMLLM_QGEMM_XRING 0
 #endif
   static constexpr int HALVES = SWARMLLM_QGEMM_HALVES;
   static constexpr int THREADS = 96 + 128 * DQ;          // W producer, MMA, X producer, DQ WGs
@@ -85,16 +90,18 @@ struct QCfg {
   static constexpr int W_STAGE = 128 * ROW_MAX;          // 18 KB for Q4_K
   static_assert(A_COL >= NACC * N, "TMEM budget");
   static constexpr int BAR_BYTES = 512;
-  // The activation tiles have their own ring, X_ST units deep, independent
-  // of the TMEM stages: their TMA loads (L2 hits, but with the latency of an
-  // SM whose HBM queue is full) run that many units ahead of the MMAs.
+  // Activation tiles: by default one per TMEM A stage, released by the same
+  // MMA commit (each tcgen05.commit costs the pipe a drain; see the MMA
+  // probe).  With SWARMLLM_QGEMM_XRING they get their own ring, X_ST units
+  // deep, released by a commit of their own.
   // Two W stages per warpgroup unless that costs X stages below 4.
   static constexpr int x_room(int w_st) {
     return (227 * 1024 - 1024 - BAR_BYTES - w_st * W_STAGE) / X_UNIT_BYTES;
   }
   static constexpr int W_ST =
       x_room(2 * DQ) >= (x_room(DQ) < 4 ? x_room(DQ) : 4) ? 2 * DQ : DQ;
-  static constexpr int X_ST = x_room(W_ST) < 8 ? x_room(W_ST) : 8;
+  static constexpr bool X_TIED = SWARMLLM_QGEMM_XRING == 0;
+  static constexpr int X_ST = X_TIED ? U : (x_room(W_ST) < 8 ? x_room(W_ST) : 8);
   static_assert(X_ST >= 2, "activation ring");
   static constexpr int X_BYTES = X_ST * X_UNIT_BYTES;
   static constexpr int W_BYTES = W_ST * W_STAGE;
@@ -157,21 +164,21 @@ SW_DEVICE bool dq_unit_fmt(const uint8_t* stage, int row, uint64_t* w_empty, uin
   F::prep(r);
 #pragma unroll
   for (int h = 0; h < H; ++h) {
-    uint32_t cols[64];
-    if (H == 2) F::dq_half(r, h, cols);
-    if (!mbar_wait_warp(&empty_h[h], empty_parity, status, 32, i, h)) return false;
-    tc_fence_after();
+    if constexpr (H == 2) {
+      uint32_t cols[64];
+      dq_half_regs<F>(r, h, cols);
+      if (!mbar_wait_warp(&empty_h[h], empty_parity, status, 32, i, h)) return false;
+      tc_fence_after();
 #if SWARMLLM_QGEMM_EXPERIMENT != 1
-    if (H == 2) {
       store_half(taddr, h, cols);
-    } else {
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        F::dq_half(r, q, cols);
-        store_half(taddr, q, cols);
-      }
-    }
 #endif
+    } else {
+      if (!mbar_wait_warp(&empty_h[h], empty_parity, status, 32, i, h)) return false;
+      tc_fence_after();
+#if SWARMLLM_QGEMM_EXPERIMENT != 1
+      dq_unit_store<F>(r, taddr);
+#endif
+    }
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
@@ -273,7 +280,9 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
       for (int i = 0; i < n_units && ok; ++i, (++sb == a.ksb) ? (sb = 0, ++tile) : 0) {
         const int nt = tile % a.n_tok_tiles;
         const int xs = i % C::X_ST;
-        if (!(ok = mbar_wait(&x_empty[xs], ((i / C::X_ST) & 1) ^ 1, a.status, 12, i, 0))) break;
+        // a tied slot is free once the unit that last used it left its A stage
+        uint64_t* free_bar = C::X_TIED ? &empty[xs * C::HALVES + C::HALVES - 1] : &x_empty[xs];
+        if (!(ok = mbar_wait(free_bar, ((i / C::X_ST) & 1) ^ 1, a.status, 12, i, 0))) break;
         mbar_arrive_expect_tx(&x_full[xs], C::X_UNIT_BYTES);
         uint8_t* dst = x_smem + xs * C::X_UNIT_BYTES;
 #pragma unroll
@@ -326,7 +335,7 @@ __global__ void __launch_bounds__(QCfg<F, FB, N>::THREADS, 1)
           umma_commit(&empty[s * C::HALVES + h]);
         }
         if (!ok) break;
-        umma_commit(&x_empty[xs]);
+        if (!C::X_TIED) umma_commit(&x_empty[xs]);
         if (last) {
           umma_commit(d_full);
           ++seg;

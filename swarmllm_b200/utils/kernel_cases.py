@@ -75,10 +75,10 @@ def run_case(which: str, TIME: bool = False, qtype: str = "Q4_K") -> None:
         iters = 2048
         for i, (ts, m, n) in enumerate(C().mma_probe_shapes()):
             cyc = torch.zeros(sms, dtype=torch.int64, device=dev)
-            C().mma_probe(i, 64, cyc)                  # warm-up
+            C().mma_probe(i, 64, cyc, 0)               # warm-up
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            C().mma_probe(i, iters, cyc)
+            C().mma_probe(i, iters, cyc, 0)
             b.record()
             torch.cuda.synchronize()
             per = float(cyc.float().median()) / (iters * 4)
@@ -86,17 +86,22 @@ def run_case(which: str, TIME: bool = False, qtype: str = "Q4_K") -> None:
             flop = 2.0 * m * n * 16 * sms / (ns * 1e-9) / 1e12
             print(f"{'TS' if ts else 'SS'} M={m:3d} N={n:3d} K=16: {per:6.1f} clk/MMA  "
                   f"{ns:6.1f} ns/MMA  {flop:7.1f} TFLOP/s (all SMs)", flush=True)
-        # the round trip of a refill: commit + wait after every 16 MMAs (one 256-K unit)
+        # what a pipeline pays around its MMAs, every `grp` MMAs: a commit (no wait),
+        # a commit + wait for completion, the same with 4 rotating accumulators,
+        # or a 1500-clock pause of the issuing thread without any commit
         for i, (ts, m, n) in enumerate(C().mma_probe_shapes()):
-            if not ts or n > 64:
+            if not ts or n != 32:
                 continue
             for grp in (4, 16, 48):
-                cyc = torch.zeros(sms, dtype=torch.int64, device=dev)
-                C().mma_probe(i, 512, cyc, grp)
-                torch.cuda.synchronize()
-                per = float(cyc.float().median()) / (512 * 4)
-                print(f"TS M={m:3d} N={n:3d}, commit+wait every {grp:2d} MMAs: {per:6.1f} clk/MMA "
-                      f"({per * grp:7.1f} clk per group)", flush=True)
+                for mode, spin, what in ((0, 0, "commit"), (1, 0, "commit+wait"),
+                                         (3, 0, "commit+wait, 4 accumulators"),
+                                         (4, 1500, "1500-clock pause")):
+                    cyc = torch.zeros(sms, dtype=torch.int64, device=dev)
+                    C().mma_probe(i, 512, cyc, grp, mode, spin)
+                    torch.cuda.synchronize()
+                    per = float(cyc.float().median()) / (512 * 4)
+                    print(f"TS M={m:3d} N={n:3d}, every {grp:2d} MMAs {what}: {per:6.1f} clk/MMA "
+                          f"({per * grp:7.1f} clk per group)", flush=True)
     elif which == "qgemm":       # Llama-3.3-70B gate|up at decode batch 32 (264 MB of weights)
         from swarmllm_b200.ops.linear import GemmWorkspace, QLinear
         rows, K, T = 57344, 8192, 32
