@@ -47,6 +47,7 @@ SW_DEVICE uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t sel) {
 struct FmtQ4K {
   static constexpr int ID = kFmtQ4K;
   static constexpr int ROW_BYTES = kQ4kRowBytes;
+  static constexpr bool HAS_I8 = true, X8_NATURAL = false;   // gemv_i8 and its x order
   struct Regs {
     uint4 q[8];
     uint4 hdr;
@@ -173,8 +174,9 @@ struct FmtQ4K {
 // sum of the 32 rounded values.  The min term uses that sum of the rounded
 // activations, so the result is exactly W . x_rounded: the rounding error is
 // not multiplied by the (all-positive) scaled codes alone.
-// xq: [T][32] uint2, xs2: [T][8] (dx, dx * sum).
-template <int T>
+// xq: [T][32] uint2, xs2: [T][8] (dx, dx * sum).  NAT: the int8 words in
+// plain K order ((0..3), (4..7)) instead, for formats with byte codes.
+template <int T, bool NAT = false>
 SW_DEVICE void quantize_x8(const uint4* xs, uint2* xq, float2* xs2, int lane) {
 #pragma unroll
   for (int t = 0; t < T; ++t) {
@@ -194,9 +196,15 @@ SW_DEVICE void quantize_x8(const uint4* xs, uint2* xq, float2* xs2, int lane) {
       sum += r - M;               // the rounded value, exactly
       return (uint32_t)__float_as_int(r) & 0xFFu;
     };
-    // low-nibble partners: K (0, 4, 1, 5); high-nibble partners: K (2, 6, 3, 7)
-    const uint32_t lo = q8(f0.x) | (q8(f2.x) << 8) | (q8(f0.y) << 16) | (q8(f2.y) << 24);
-    const uint32_t hi = q8(f1.x) | (q8(f3.x) << 8) | (q8(f1.y) << 16) | (q8(f3.y) << 24);
+    uint32_t lo, hi;
+    if constexpr (NAT) {
+      lo = q8(f0.x) | (q8(f0.y) << 8) | (q8(f1.x) << 16) | (q8(f1.y) << 24);
+      hi = q8(f2.x) | (q8(f2.y) << 8) | (q8(f3.x) << 16) | (q8(f3.y) << 24);
+    } else {
+      // low-nibble partners: K (0, 4, 1, 5); high-nibble partners: K (2, 6, 3, 7)
+      lo = q8(f0.x) | (q8(f2.x) << 8) | (q8(f0.y) << 16) | (q8(f2.y) << 24);
+      hi = q8(f1.x) | (q8(f3.x) << 8) | (q8(f1.y) << 16) | (q8(f3.y) << 24);
+    }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     xq[t * 32 + lane] = make_uint2(lo, hi);
@@ -229,6 +237,7 @@ SW_DEVICE void q6k_word(uint32_t x, uint32_t h, __half2 (&c)[4]) {
 struct FmtQ6K {
   static constexpr int ID = kFmtQ6K;
   static constexpr int ROW_BYTES = kQ6kRowBytes;
+  static constexpr bool HAS_I8 = false, X8_NATURAL = false;
   struct Regs {
     uint4 lo[8];   // 32 low-nibble words
     uint4 hc[4];   // 16 crumb words
@@ -316,6 +325,7 @@ SW_DEVICE void q80_word(uint32_t x, __half2 D, uint32_t* out) {
 struct FmtQ80 {
   static constexpr int ID = kFmtQ8_0;
   static constexpr int ROW_BYTES = kQ80RowBytes;
+  static constexpr bool HAS_I8 = true, X8_NATURAL = true;
   struct Regs {
     uint4 q[16];   // 64 code words
     uint4 d;       // 8 fp16 block scales
@@ -335,6 +345,36 @@ struct FmtQ80 {
 #pragma unroll
     for (int w = 0; w < 8; ++w) q80_word(qw[8 * b + w], D, out + 2 * w);
   }
+  // Integer-dot variant (activations quantized per 32 values in plain K
+  // order): per 32-value block 8 dp4a of the signed codes (u ^ 0x80) and the
+  // int8 activations, then d * dx in fp32.
+  template <int T>
+  static SW_DEVICE void gemv_i8(const Regs& r, const uint2* xq, const float2* xs2,
+                                float (&acc)[T]) {
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(r.q);
+    const __half* dh = reinterpret_cast<const __half*>(&r.d);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      int is[T];
+#pragma unroll
+      for (int t = 0; t < T; ++t) is[t] = 0;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const int c0 = (int)(qw[8 * b + 2 * v] ^ 0x80808080u);
+        const int c1 = (int)(qw[8 * b + 2 * v + 1] ^ 0x80808080u);
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const uint2 xv = xq[t * 32 + 4 * b + v];
+          is[t] = __dp4a(c0, (int)xv.x, is[t]);
+          is[t] = __dp4a(c1, (int)xv.y, is[t]);
+        }
+      }
+      const float d = __half2float(dh[b]);
+#pragma unroll
+      for (int t = 0; t < T; ++t) acc[t] = fmaf(d * xs2[t * 8 + b].x, (float)is[t], acc[t]);
+    }
+  }
+
   // Weights are scaled before the products (q*d is what the tensor-core path
   // multiplies too), so the fp16 partials hold ordinary w*x sums.
   template <int T>

@@ -27,8 +27,9 @@
 // weights in fp32 (qfmt.cuh FmtQ4K::gemv_i8).  That is about 5 issue slots
 // per 8 weights instead of 13 for fp16 dequantization, so the weight stream
 // is no longer issue-bound; the activation rounding adds ~0.5 % relative
-// error.  SWARMLLM_GEMV_I8=0 selects the fp16 path (FmtQ4K::gemv), which the
-// other formats always take.
+// error.  Q8_0 does the same with its byte codes (activations in plain K
+// order).  SWARMLLM_GEMV_I8=0 selects the fp16 paths (F::gemv), which Q6_K
+// always takes.
 #include "kernels.h"
 
 #include <cstdlib>
@@ -101,7 +102,7 @@ SW_DEVICE bool gemv_unit(const uint8_t* stage, uint64_t* xb, const uint8_t* xsta
   if constexpr (I8) {
     uint2* xq8 = reinterpret_cast<uint2*>(xq);
     float2* xs2 = reinterpret_cast<float2*>(xq + T * 256);
-    quantize_x8<T>(reinterpret_cast<const uint4*>(xstage), xq8, xs2, lane);
+    quantize_x8<T, F::X8_NATURAL>(reinterpret_cast<const uint4*>(xstage), xq8, xs2, lane);
     __syncwarp();
     F::template gemv_i8<T>(r, xq8, xs2, acc);
   } else {
@@ -257,7 +258,7 @@ static int setup_t() {
 
 template <class F, int T>
 static int occupancy_t() {
-  constexpr bool I8 = F::ID == kFmtQ4K;
+  constexpr bool I8 = F::HAS_I8;
   if (setup_t<F, F, T, I8>() != 1) return -1;
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, qgemv_q4k_kernel<F, F, T, I8>,
@@ -276,7 +277,7 @@ static int launch_t(const GemvArgs& a, int ctas, cudaStream_t s) {
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
-// Q4_K (unmixed) takes the integer-dot variant unless SWARMLLM_GEMV_I8=0.
+// Q4_K and Q8_0 (unmixed) take the integer-dot variant unless SWARMLLM_GEMV_I8=0.
 static const bool g_gemv_i8 = [] {
   const char* v = getenv("SWARMLLM_GEMV_I8");
   return v ? atoi(v) != 0 : true;
@@ -284,7 +285,7 @@ static const bool g_gemv_i8 = [] {
 
 template <class F, class FB = F>
 static int launch_f(const GemvArgs& a, int T, int ctas, cudaStream_t s) {
-  if constexpr (F::ID == kFmtQ4K && std::is_same<F, FB>::value) {
+  if constexpr (F::HAS_I8 && std::is_same<F, FB>::value) {
     if (g_gemv_i8)
       return T == 1 ? launch_t<F, FB, 1, true>(a, ctas, s) : launch_t<F, FB, 2, true>(a, ctas, s);
   }
