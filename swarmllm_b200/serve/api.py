@@ -287,7 +287,11 @@ class Serving:
         constraint = None
         if isinstance(rf, dict) and rf.get("type") in ("json_object", "json_schema"):
             from .json_guard import JsonConstraint
-            constraint = JsonConstraint(self.piece, int(self.eos))
+            schema = None
+            if rf.get("type") == "json_schema":
+                schema = (rf.get("json_schema") or {}).get("schema")
+            constraint = JsonConstraint(self.piece, int(self.eos),
+                                        schema=schema if isinstance(schema, dict) else None)
         bias = None
         lb = body.get("logit_bias")
         if lb:

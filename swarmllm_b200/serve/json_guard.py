@@ -7,9 +7,9 @@ engine step: of the sampled row's candidates (the drawn token first, then the
 others by logit) it keeps the first whose text leaves the output a valid JSON
 prefix; the end-of-sequence token is allowed only once the top-level value is
 complete, and forced then.  The output is therefore always a prefix of valid
-JSON, and valid JSON when the model stops on its own.  A json_schema's
-structure is asked for in the prompt; the constraint enforces JSON syntax and
-a top-level object.
+JSON, and valid JSON when the model stops on its own.  With a json_schema the
+recogniser is schema_guard.SchemaPrefix, which also enforces the schema's
+types, keys, required properties, items, enums and alternatives.
 
 Reference behaviour: reply grammar via llguidance (src/inference/reply_grammar.rs:156,240).
 """
@@ -186,16 +186,22 @@ class JsonPrefix:
 
 
 class JsonConstraint:
-    """Per-request state of JSON-constrained decoding."""
+    """Per-request state of JSON-constrained decoding (JSON syntax, or a JSON
+    schema when one is given)."""
 
-    def __init__(self, piece, eos_id: int, top_object: bool = True):
+    def __init__(self, piece, eos_id: int, top_object: bool = True, schema: dict | None = None):
         self.piece = piece              # token id -> its text
         self.eos = eos_id
-        self.state = JsonPrefix(top_object)
+        self.schema = schema
+        if schema is not None:
+            from .schema_guard import SchemaPrefix
+            self.state = SchemaPrefix(schema)
+        else:
+            self.state = JsonPrefix(top_object)
 
     def fresh(self) -> "JsonConstraint":
         """The same constraint from the start (one per request)."""
-        return JsonConstraint(self.piece, self.eos, self.state.top_object)
+        return JsonConstraint(self.piece, self.eos, self.state.top_object, self.schema)
 
     def allowed(self, tok: int) -> bool:
         if tok == self.eos:
