@@ -237,7 +237,7 @@ SW_DEVICE void q6k_word(uint32_t x, uint32_t h, __half2 (&c)[4]) {
 struct FmtQ6K {
   static constexpr int ID = kFmtQ6K;
   static constexpr int ROW_BYTES = kQ6kRowBytes;
-  static constexpr bool HAS_I8 = false, X8_NATURAL = false;
+  static constexpr bool HAS_I8 = true, X8_NATURAL = false;
   struct Regs {
     uint4 lo[8];   // 32 low-nibble words
     uint4 hc[4];   // 16 crumb words
@@ -273,6 +273,44 @@ struct FmtQ6K {
       }
     }
   }
+  // Integer-dot variant: the 6-bit codes of a word rebuilt as bytes in the
+  // repacked nibble order (low nibble | crumb << 4: the crumbs of K' = 0, 4,
+  // 1, 5 sit at bits 0, 4, 16, 20 of the crumb word, those of 2, 6, 3, 7 two
+  // bits higher), minus 32 per byte, then dp4a against the int8 activations;
+  // the fp16 sub-block scale (16 values) times the activation scale (32
+  // values) in fp32.
+  template <int T>
+  static SW_DEVICE void gemv_i8(const Regs& r, const uint2* xq, const float2* xs2,
+                                float (&acc)[T]) {
+    const uint32_t* lw = reinterpret_cast<const uint32_t*>(r.lo);
+    const uint32_t* hw = reinterpret_cast<const uint32_t*>(r.hc);
+    const __half* sh = reinterpret_cast<const __half*>(r.sc);
+#pragma unroll
+    for (int s = 0; s < 16; ++s) {
+      int is[T];
+#pragma unroll
+      for (int t = 0; t < T; ++t) is[t] = 0;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t x = lw[2 * s + e], h = e ? hw[s] >> 8 : hw[s];
+        const uint32_t lo = and_or(h << 8, 0x30003000u,
+                                   and_or(h << 4, 0x00300030u, x & 0x0F0F0F0Fu));
+        const uint32_t hi = and_or(h << 6, 0x30003000u,
+                                   and_or(h << 2, 0x00300030u, (x >> 4) & 0x0F0F0F0Fu));
+        const int slo = (int)__vsub4(lo, 0x20202020u), shi = (int)__vsub4(hi, 0x20202020u);
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const uint2 v = xq[t * 32 + 2 * s + e];
+          is[t] = __dp4a(slo, (int)v.x, is[t]);
+          is[t] = __dp4a(shi, (int)v.y, is[t]);
+        }
+      }
+      const float S = __half2float(sh[s]);
+#pragma unroll
+      for (int t = 0; t < T; ++t) acc[t] = fmaf(S * xs2[t * 8 + (s >> 1)].x, (float)is[t], acc[t]);
+    }
+  }
+
   // (q - 32) x products in fp16: two per partial sum (|sum| <= 64 |x|max),
   // then the sub-block scale in fp32.
   template <int T>

@@ -28,8 +28,8 @@
 // per 8 weights instead of 13 for fp16 dequantization, so the weight stream
 // is no longer issue-bound; the activation rounding adds ~0.5 % relative
 // error.  Q8_0 does the same with its byte codes (activations in plain K
-// order).  SWARMLLM_GEMV_I8=0 selects the fp16 paths (F::gemv), which Q6_K
-// always takes.
+// order), Q6_K with its 6-bit codes rebuilt as bytes.  SWARMLLM_GEMV_I8=0
+// selects the fp16 paths (F::gemv); the mixed Q4_K|Q6_K GEMV always takes them.
 #include "kernels.h"
 
 #include <cstdlib>
@@ -277,7 +277,7 @@ static int launch_t(const GemvArgs& a, int ctas, cudaStream_t s) {
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 
-// Q4_K and Q8_0 (unmixed) take the integer-dot variant unless SWARMLLM_GEMV_I8=0.
+// Q4_K, Q6_K and Q8_0 (unmixed) take the integer-dot variant unless SWARMLLM_GEMV_I8=0.
 static const bool g_gemv_i8 = [] {
   const char* v = getenv("SWARMLLM_GEMV_I8");
   return v ? atoi(v) != 0 : true;

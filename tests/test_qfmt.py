@@ -87,3 +87,28 @@ def test_repacked_layout_dequantizes(qt, fmt):
     rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
     assert rel < (1e-3 if fmt == 1 else 1e-7), rel
     assert not pk[1, :, rows - 128:].any()                # padding rows are zero
+
+
+def test_q6k_int8_bytes_match_codes():
+    """Mirror of FmtQ6K::gemv_i8's byte rebuild: low nibbles with their crumbs
+    shifted into each byte lane, in the int8 activations' order (K' = 0,4,1,5
+    and 2,6,3,7), minus 32."""
+    rng = np.random.default_rng(5)
+    rows, K = 128, 256
+    b = Q.quantize(rng.standard_normal((rows, K), dtype=np.float32) * 0.03, Q.Q6_K)
+    codes = Q._q6k_codes(b.reshape(rows, 1, 210)).reshape(rows, K).astype(np.int64) - 32
+    pk = Q.q6k_repack_host(b, rows, K)
+    for r in (0, 5, 127):
+        row = pk[0, 0, r]
+        lo = row[:128].copy().view(np.uint32)
+        cr = row[128:192].copy().view(np.uint32)
+        for s in range(16):
+            for e in range(2):
+                x, h = int(lo[2 * s + e]), (int(cr[s]) >> 8 if e else int(cr[s]))
+                L = ((h << 8) & 0x30003000) | ((h << 4) & 0x00300030) | (x & 0x0F0F0F0F)
+                H = ((h << 6) & 0x30003000) | ((h << 2) & 0x00300030) | ((x >> 4) & 0x0F0F0F0F)
+                got_lo = [((L >> (8 * i)) & 0xFF) - 32 for i in range(4)]
+                got_hi = [((H >> (8 * i)) & 0xFF) - 32 for i in range(4)]
+                base = 16 * s + 8 * e
+                assert got_lo == [codes[r, base + k] for k in (0, 4, 1, 5)]
+                assert got_hi == [codes[r, base + k] for k in (2, 6, 3, 7)]
