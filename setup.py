@@ -74,7 +74,8 @@ ext_modules.append(
         name="swarmllm_b200._native",
         sources=native_sources,
         include_dirs=[pybind11.get_include(), os.path.join(ROOT, CSRC, "native")],
-        extra_compile_args=CXX_FLAGS + ["-fvisibility=hidden", "-Wall"],
+        extra_compile_args=CXX_FLAGS + ["-fvisibility=hidden", "-Wall", "-fopenmp"],
+        extra_link_args=["-fopenmp"],
         language="c++",
     )
 )

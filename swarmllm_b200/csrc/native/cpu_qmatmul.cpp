@@ -1,0 +1,396 @@
+// Quantized matmul on the host CPU: out[t][r] = sum_k W[r][k] * x[t][k] with W
+// in its GGUF blocks (Q4_K, Q6_K, Q8_0), never dequantized to a float matrix.
+//
+// The activations of every token are quantized once per call to int8 with one
+// scale per 32 values (absmax / 127, round to nearest), and each block's dot
+// product is an int8 x int8 -> int32 loop the compiler vectorises; the block
+// and sub-block scales are applied in fp32:
+//   Q8_0  sum_b d_b dx_b sum q x
+//   Q6_K  sum_s d sc_s dx sum (q - 32) x                (16-value sub-blocks)
+//   Q4_K  sum_j d sc_j dx_j sum q x - dmin m_j dx_j sum x  (32-value sub-blocks)
+// with the min term over the rounded activations, so the result is exactly
+// W . x_rounded.  Rows are split over OpenMP threads.
+//
+// On CPUs with AVX-512 VNNI (picked at run time) the codes of each 64-value
+// group go through one vpdpbusd (unsigned codes x signed activations, four
+// products per 32-bit lane) per token; a lane's partial sum is scaled in fp32
+// by its sub-block's scale times its activation block's scale, so all three
+// formats share one inner loop and differ only in how a block is unpacked:
+// Q4_K codes are already unsigned, Q6_K codes are used before their -32 and
+// Q8_0 codes are flipped to q + 128; the offsets come back as one correction
+// per block against the sums of the rounded activations.  This is the CPU
+// inference path of a node without a GPU (the reference's CPU kernels:
+// src/inference/split/attn_rows.rs, fast_math.rs); the fp32 PyTorch model
+// stays the numerical oracle.
+#include "cpu_qmatmul.h"
+
+#include <immintrin.h>
+
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+namespace swarm_native {
+namespace {
+
+inline float half_to_float(uint16_t h) {
+  const uint32_t s = (uint32_t)(h >> 15) << 31;
+  uint32_t e = (h >> 10) & 0x1F, m = h & 0x3FF;
+  uint32_t bits;
+  if (e == 0) {
+    if (m == 0) {
+      bits = s;
+    } else {  // subnormal: normalise
+      e = 127 - 15 + 1;
+      while (!(m & 0x400)) {
+        m <<= 1;
+        --e;
+      }
+      bits = s | (e << 23) | ((m & 0x3FF) << 13);
+    }
+  } else if (e == 31) {
+    bits = s | 0x7F800000u | (m << 13);
+  } else {
+    bits = s | ((e + 127 - 15) << 23) | (m << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+inline uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+// x [K] -> int8 [K], dx [K/32] scales, sx [K/32] sums of the rounded values
+void quantize_row(const float* x, int K, int8_t* q, float* dx, int32_t* sx) {
+  for (int b = 0; b < K / 32; ++b) {
+    const float* xb = x + 32 * b;
+    float amax = 0.f;
+    for (int i = 0; i < 32; ++i) amax = std::fmax(amax, std::fabs(xb[i]));
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+    int32_t s = 0;
+    for (int i = 0; i < 32; ++i) {
+      const int v = (int)std::nearbyint(xb[i] * inv);
+      q[32 * b + i] = (int8_t)v;
+      s += v;
+    }
+    dx[b] = amax / 127.f;
+    sx[b] = s;
+  }
+}
+
+inline int32_t dot_i8(const int8_t* a, const int8_t* b, int n) {
+  int32_t s = 0;
+  for (int i = 0; i < n; ++i) s += (int32_t)a[i] * (int32_t)b[i];
+  return s;
+}
+
+// Token tile: a block's codes are unpacked once and dotted with this many
+// tokens' activations before the next block.
+constexpr int kTT = 8;
+
+struct Acts {
+  const int8_t* q;    // [T, K]
+  const float* dx;    // [T, K/32]
+  const int32_t* sx;  // [T, K/32]
+  int K;
+};
+
+// One Q4_K block (256 values, 144 bytes) against tokens t0..t0+nt.
+void block_q4k(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
+  const float d = half_to_float(rd16(blk)), dmin = half_to_float(rd16(blk + 2));
+  const uint8_t* sc = blk + 4;
+  const uint8_t* qs = blk + 16;
+  alignas(64) int8_t q[256];
+  for (int g = 0; g < 4; ++g)
+    for (int l = 0; l < 32; ++l) {
+      q[64 * g + l] = (int8_t)(qs[32 * g + l] & 0xF);
+      q[64 * g + 32 + l] = (int8_t)(qs[32 * g + l] >> 4);
+    }
+  float ds[8], dm[8];
+  for (int j = 0; j < 8; ++j) {
+    int s, m;
+    if (j < 4) {
+      s = sc[j] & 63;
+      m = sc[j + 4] & 63;
+    } else {
+      s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+      m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    ds[j] = d * (float)s;
+    dm[j] = dmin * (float)m;
+  }
+  const int nb = a.K / 32;
+  for (int t = 0; t < nt; ++t) {
+    const int8_t* xq = a.q + (size_t)(t0 + t) * a.K + 256 * b;
+    const float* dx = a.dx + (size_t)(t0 + t) * nb + 8 * b;
+    const int32_t* sx = a.sx + (size_t)(t0 + t) * nb + 8 * b;
+    float v = 0.f;
+    for (int j = 0; j < 8; ++j)
+      v += dx[j] * (ds[j] * (float)dot_i8(q + 32 * j, xq + 32 * j, 32) - dm[j] * (float)sx[j]);
+    acc[t] += v;
+  }
+}
+
+// One Q6_K block (256 values, 210 bytes).
+void block_q6k(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
+  const uint8_t* ql = blk;
+  const uint8_t* qh = blk + 128;
+  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+  const float d = half_to_float(rd16(blk + 208));
+  alignas(64) int8_t q[256];
+  for (int n = 0; n < 2; ++n)
+    for (int l = 0; l < 32; ++l) {
+      const int h = qh[32 * n + l];
+      const int l0 = ql[64 * n + l], l1 = ql[64 * n + 32 + l];
+      q[128 * n + l] = (int8_t)(((l0 & 0xF) | ((h & 3) << 4)) - 32);
+      q[128 * n + 32 + l] = (int8_t)(((l1 & 0xF) | (((h >> 2) & 3) << 4)) - 32);
+      q[128 * n + 64 + l] = (int8_t)(((l0 >> 4) | (((h >> 4) & 3) << 4)) - 32);
+      q[128 * n + 96 + l] = (int8_t)(((l1 >> 4) | (((h >> 6) & 3) << 4)) - 32);
+    }
+  float ds[16];
+  for (int s = 0; s < 16; ++s) ds[s] = d * (float)sc[s];
+  const int nb = a.K / 32;
+  for (int t = 0; t < nt; ++t) {
+    const int8_t* xq = a.q + (size_t)(t0 + t) * a.K + 256 * b;
+    const float* dx = a.dx + (size_t)(t0 + t) * nb + 8 * b;
+    float v = 0.f;
+    for (int s = 0; s < 16; ++s) v += ds[s] * dx[s >> 1] * (float)dot_i8(q + 16 * s, xq + 16 * s, 16);
+    acc[t] += v;
+  }
+}
+
+// One Q8_0 block (32 values, 34 bytes).
+void block_q80(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
+  const float d = half_to_float(rd16(blk));
+  const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
+  const int nb = a.K / 32;
+  for (int t = 0; t < nt; ++t)
+    acc[t] += d * a.dx[(size_t)(t0 + t) * nb + b] *
+              (float)dot_i8(q, a.q + (size_t)(t0 + t) * a.K + 32 * b, 32);
+}
+
+// ---------------------------------------------------------------- AVX-512 VNNI
+#define SWARM_VNNI __attribute__((target("avx512f,avx512bw,avx512dq,avx512vl,avx512vnni")))
+
+// Lane i of a 64-value group g holds values 64g + 4i .. 64g + 4i + 3, whose
+// activation block is 2g + (i >= 8).
+struct ActsX {
+  const int8_t* q;      // [T, K]
+  const float* dx;      // [T, K/32]
+  const float* dxs;     // [T, K/32]: dx * (sum of the rounded values), per 32
+  const float* dxs16;   // [T, K/16]: dx * (sum of the rounded values), per 16
+  int K;
+};
+
+// One 256-value block unpacked for the shared loop: unsigned codes of the four
+// 64-value groups, the per-lane weight scales, and the offset correction
+// `corr` dotted with the activation sums (8 per-32 sums, or 16 per-16 sums).
+struct Unpacked {
+  __m512i c[4];
+  __m512 s[4];
+  __m512 corr;  // Q6_K: 16 lanes; Q4_K / Q8_0: lanes 0-7
+};
+
+SWARM_VNNI inline __m512 halves(float a, float b) {
+  return _mm512_insertf32x8(_mm512_castps256_ps512(_mm256_set1_ps(a)), _mm256_set1_ps(b), 1);
+}
+
+SWARM_VNNI inline void unpack_q4k(const uint8_t* blk, Unpacked& u) {
+  const float d = half_to_float(rd16(blk)), dmin = half_to_float(rd16(blk + 2));
+  const uint8_t* sc = blk + 4;
+  const uint8_t* qs = blk + 16;
+  float ds[8], dm[8];
+  for (int j = 0; j < 8; ++j) {
+    int s, m;
+    if (j < 4) {
+      s = sc[j] & 63;
+      m = sc[j + 4] & 63;
+    } else {
+      s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+      m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    ds[j] = d * (float)s;
+    dm[j] = dmin * (float)m;
+  }
+  const __m256i lo4 = _mm256_set1_epi8(0x0F);
+  for (int g = 0; g < 4; ++g) {
+    const __m256i v = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(qs + 32 * g));
+    const __m256i lo = _mm256_and_si256(v, lo4);
+    const __m256i hi = _mm256_and_si256(_mm256_srli_epi16(v, 4), lo4);
+    u.c[g] = _mm512_inserti64x4(_mm512_castsi256_si512(lo), hi, 1);
+    u.s[g] = halves(ds[2 * g], ds[2 * g + 1]);
+  }
+  u.corr = _mm512_castps256_ps512(_mm256_loadu_ps(dm));
+}
+
+// bits sh, sh+1 of every qh byte, moved to bits 4-5
+SWARM_VNNI inline __m256i q6_hi(__m256i h, int sh, __m256i two) {
+  return _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(h, sh), two), 4);
+}
+
+SWARM_VNNI inline void unpack_q6k(const uint8_t* blk, Unpacked& u) {
+  const uint8_t* ql = blk;
+  const uint8_t* qh = blk + 128;
+  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+  const float d = half_to_float(rd16(blk + 208));
+  alignas(64) float ds[16];
+  for (int i = 0; i < 16; ++i) ds[i] = d * (float)sc[i];
+  const __m256i lo4 = _mm256_set1_epi8(0x0F), two = _mm256_set1_epi8(0x03);
+  for (int n = 0; n < 2; ++n) {
+    const __m256i l0 = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(ql + 64 * n));
+    const __m256i l1 = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(ql + 64 * n + 32));
+    const __m256i h = _mm256_loadu_si256(reinterpret_cast<const __m256i*>(qh + 32 * n));
+    const __m256i q0 = _mm256_or_si256(_mm256_and_si256(l0, lo4), q6_hi(h, 0, two));
+    const __m256i q1 = _mm256_or_si256(_mm256_and_si256(l1, lo4), q6_hi(h, 2, two));
+    const __m256i q2 =
+        _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(l0, 4), lo4), q6_hi(h, 4, two));
+    const __m256i q3 =
+        _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(l1, 4), lo4), q6_hi(h, 6, two));
+    u.c[2 * n] = _mm512_inserti64x4(_mm512_castsi256_si512(q0), q1, 1);
+    u.c[2 * n + 1] = _mm512_inserti64x4(_mm512_castsi256_si512(q2), q3, 1);
+  }
+  // lane i of group g covers values 64g + 4i..: sub-block 4g + i / 4
+  const __m512i rep4 = _mm512_set_epi32(3, 3, 3, 3, 2, 2, 2, 2, 1, 1, 1, 1, 0, 0, 0, 0);
+  for (int g = 0; g < 4; ++g)
+    u.s[g] = _mm512_permutexvar_ps(rep4, _mm512_castps128_ps512(_mm_loadu_ps(ds + 4 * g)));
+  u.corr = _mm512_mul_ps(_mm512_load_ps(ds), _mm512_set1_ps(32.f));
+}
+
+// Eight Q8_0 blocks (256 values, 8 x 34 bytes), codes flipped to q + 128.
+SWARM_VNNI inline void unpack_q80x8(const uint8_t* blk, Unpacked& u) {
+  float d[8];
+  const __m256i flip = _mm256_set1_epi8((char)0x80);
+  for (int j = 0; j < 8; ++j) d[j] = half_to_float(rd16(blk + 34 * j));
+  for (int g = 0; g < 4; ++g) {
+    const __m256i a = _mm256_xor_si256(
+        _mm256_loadu_si256(reinterpret_cast<const __m256i*>(blk + 34 * (2 * g) + 2)), flip);
+    const __m256i b = _mm256_xor_si256(
+        _mm256_loadu_si256(reinterpret_cast<const __m256i*>(blk + 34 * (2 * g + 1) + 2)), flip);
+    u.c[g] = _mm512_inserti64x4(_mm512_castsi256_si512(a), b, 1);
+    u.s[g] = halves(d[2 * g], d[2 * g + 1]);
+  }
+  u.corr = _mm512_mul_ps(_mm512_castps256_ps512(_mm256_loadu_ps(d)), _mm512_set1_ps(128.f));
+}
+
+// out[t] for tokens t0..t0+nt of one weight row; FMT 0 Q4_K, 1 Q6_K, 2 Q8_0.
+template <int FMT>
+SWARM_VNNI void row_vnni(const uint8_t* wr, int nsb, const ActsX& a, int t0, int nt, float* res) {
+  constexpr size_t SB_BYTES = FMT == 0 ? 144 : FMT == 1 ? 210 : 8 * 34;
+  __m512 facc[kTT], cacc[kTT];
+  for (int t = 0; t < nt; ++t) facc[t] = cacc[t] = _mm512_setzero_ps();
+  // lanes 0-7 take the group's first activation scale, lanes 8-15 its second
+  const __m512i pair = _mm512_set_epi32(1, 1, 1, 1, 1, 1, 1, 1, 0, 0, 0, 0, 0, 0, 0, 0);
+  const int K = a.K;
+  for (int b = 0; b < nsb; ++b) {
+    Unpacked u;
+    if constexpr (FMT == 0) unpack_q4k(wr + b * SB_BYTES, u);
+    else if constexpr (FMT == 1) unpack_q6k(wr + b * SB_BYTES, u);
+    else unpack_q80x8(wr + b * SB_BYTES, u);
+    for (int t = 0; t < nt; ++t) {
+      const size_t tt = (size_t)(t0 + t);
+      const int8_t* xq = a.q + tt * K + 256 * b;
+      const float* dx = a.dx + tt * (K / 32) + 8 * b;
+      __m512 f = facc[t];
+      for (int g = 0; g < 4; ++g) {
+        const __m512i xv = _mm512_loadu_si512(xq + 64 * g);
+        const __m512i p = _mm512_dpbusd_epi32(_mm512_setzero_si512(), u.c[g], xv);
+        const __m512 dxg = _mm512_permutexvar_ps(
+            pair, _mm512_castpd_ps(_mm512_castpd128_pd512(_mm_load_sd(reinterpret_cast<const double*>(dx + 2 * g)))));
+        const __m512 sc = _mm512_mul_ps(u.s[g], dxg);
+        f = _mm512_fmadd_ps(_mm512_cvtepi32_ps(p), sc, f);
+      }
+      facc[t] = f;
+      const __m512 sums = FMT == 1 ? _mm512_loadu_ps(a.dxs16 + tt * (K / 16) + 16 * b)
+                                   : _mm512_castps256_ps512(_mm256_loadu_ps(a.dxs + tt * (K / 32) + 8 * b));
+      const __m512 cm = FMT == 1 ? u.corr : _mm512_maskz_mov_ps(0x00FF, u.corr);
+      cacc[t] = _mm512_fmadd_ps(cm, _mm512_maskz_mov_ps(FMT == 1 ? 0xFFFF : 0x00FF, sums), cacc[t]);
+    }
+  }
+  for (int t = 0; t < nt; ++t) res[t] = _mm512_reduce_add_ps(_mm512_sub_ps(facc[t], cacc[t]));
+}
+
+SWARM_VNNI void matmul_vnni(const uint8_t* w, int type, int rows, int K, const Acts& acts, int T,
+                            float* out) {
+  // the activation sums the offset corrections are dotted with
+  std::vector<float> dxs((size_t)T * (K / 32)), dxs16((size_t)T * (K / 16));
+  for (int t = 0; t < T; ++t) {
+    const float* dx = acts.dx + (size_t)t * (K / 32);
+    const int32_t* sx = acts.sx + (size_t)t * (K / 32);
+    const int8_t* q = acts.q + (size_t)t * K;
+    for (int j = 0; j < K / 32; ++j) dxs[(size_t)t * (K / 32) + j] = dx[j] * (float)sx[j];
+    for (int j = 0; j < K / 16; ++j) {
+      int32_t s16 = 0;
+      for (int i = 0; i < 16; ++i) s16 += q[16 * j + i];
+      dxs16[(size_t)t * (K / 16) + j] = dx[j / 2] * (float)s16;
+    }
+  }
+  const ActsX ax{acts.q, acts.dx, dxs.data(), dxs16.data(), K};
+  const size_t row_bytes = type == kGgmlQ4_K   ? (size_t)K / 256 * 144
+                           : type == kGgmlQ6_K ? (size_t)K / 256 * 210
+                                               : (size_t)K / 32 * 34;
+  const int nsb = K / 256;
+  auto* fn = type == kGgmlQ4_K ? row_vnni<0> : type == kGgmlQ6_K ? row_vnni<1> : row_vnni<2>;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < rows; ++r) {
+    const uint8_t* wr = w + (size_t)r * row_bytes;
+    for (int t0 = 0; t0 < T; t0 += kTT) {
+      const int nt = T - t0 < kTT ? T - t0 : kTT;
+      float res[kTT];
+      fn(wr, nsb, ax, t0, nt, res);
+      for (int t = 0; t < nt; ++t) out[(size_t)(t0 + t) * rows + r] = res[t];
+    }
+  }
+}
+
+bool use_vnni() {
+  static const bool ok = [] {
+    const char* e = std::getenv("SWARMLLM_CPU_ISA");
+    if (e && std::strcmp(e, "generic") == 0) return false;
+    __builtin_cpu_init();
+    return __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
+           __builtin_cpu_supports("avx512dq") && __builtin_cpu_supports("avx512vl") &&
+           __builtin_cpu_supports("avx512vnni");
+  }();
+  return ok;
+}
+
+}  // namespace
+
+const char* cpu_qmatmul_isa() { return use_vnni() ? "avx512vnni" : "generic"; }
+
+int cpu_qmatmul(const uint8_t* w, int type, int rows, int K, const float* x, int T,
+                float* out) {
+  if (K % 256 != 0 && !(type == kGgmlQ8_0 && K % 32 == 0)) return -1;
+  if (type != kGgmlQ4_K && type != kGgmlQ6_K && type != kGgmlQ8_0) return -2;
+  std::vector<int8_t> xq((size_t)T * K);
+  std::vector<float> dx((size_t)T * (K / 32));
+  std::vector<int32_t> sx((size_t)T * (K / 32));
+  for (int t = 0; t < T; ++t)
+    quantize_row(x + (size_t)t * K, K, xq.data() + (size_t)t * K, dx.data() + (size_t)t * (K / 32),
+                 sx.data() + (size_t)t * (K / 32));
+  const Acts acts{xq.data(), dx.data(), sx.data(), K};
+  if (K % 256 == 0 && use_vnni()) {
+    matmul_vnni(w, type, rows, K, acts, T, out);
+    return 0;
+  }
+  const size_t row_bytes = type == kGgmlQ4_K   ? (size_t)K / 256 * 144
+                           : type == kGgmlQ6_K ? (size_t)K / 256 * 210
+                                               : (size_t)K / 32 * 34;
+  const int nblk = type == kGgmlQ8_0 ? K / 32 : K / 256;
+  const size_t blk_bytes = type == kGgmlQ4_K ? 144 : type == kGgmlQ6_K ? 210 : 34;
+  auto* fn = type == kGgmlQ4_K ? block_q4k : type == kGgmlQ6_K ? block_q6k : block_q80;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < rows; ++r) {
+    const uint8_t* wr = w + (size_t)r * row_bytes;
+    for (int t0 = 0; t0 < T; t0 += kTT) {
+      const int nt = T - t0 < kTT ? T - t0 : kTT;
+      float acc[kTT] = {};
+      for (int b = 0; b < nblk; ++b) fn(wr + (size_t)b * blk_bytes, b, acts, t0, nt, acc);
+      for (int t = 0; t < nt; ++t) out[(size_t)(t0 + t) * rows + r] = acc[t];
+    }
+  }
+  return 0;
+}
+
+}  // namespace swarm_native

@@ -3,7 +3,11 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include <optional>
+
 #include "block_manager.h"
+#include "cpu_attn.h"
+#include "cpu_qmatmul.h"
 #include "gguf_reader.h"
 #include "planner.h"
 #include "scheduler.h"
@@ -88,6 +92,103 @@ PYBIND11_MODULE(_native, m) {
       .def_property_readonly("num_running", &Scheduler::num_running)
       .def_property_readonly("num_preemptions", &Scheduler::num_preemptions)
       .def("has_work", &Scheduler::has_work);
+
+  m.def(
+      "cpu_qmatmul",
+      [](py::array_t<uint8_t, py::array::c_style> w, int type, int rows, int K,
+         py::array_t<float, py::array::c_style | py::array::forcecast> x) {
+        if (x.ndim() != 2 || x.shape(1) != K) throw std::invalid_argument("x must be [T, K]");
+        const int T = (int)x.shape(0);
+        py::array_t<float> out({(py::ssize_t)T, (py::ssize_t)rows});
+        const uint8_t* wp = w.data();
+        const float* xp = x.data();
+        float* op = out.mutable_data();
+        int rc;
+        {
+          py::gil_scoped_release nogil;
+          rc = cpu_qmatmul(wp, type, rows, K, xp, T, op);
+        }
+        if (rc != 0) throw std::invalid_argument("cpu_qmatmul: unsupported type or K");
+        return out;
+      },
+      py::arg("w"), py::arg("type"), py::arg("rows"), py::arg("K"), py::arg("x"),
+      "x [T, K] fp32 times the GGUF-quantized W [rows, K]^T, int8 activations, OpenMP rows");
+  m.def("cpu_qmatmul_isa", [] { return std::string(cpu_qmatmul_isa()); });
+
+  using f32a = py::array_t<float, py::array::c_style | py::array::forcecast>;
+  using i32a = py::array_t<int32_t, py::array::c_style | py::array::forcecast>;
+  m.def(
+      "cpu_paged_attention",
+      [](f32a q, py::array k_cache, py::array v_cache, i32a block_table, i32a seq_lens,
+         float scale, int window, float softcap, std::optional<i32a> tree_start,
+         std::optional<py::array_t<int64_t, py::array::c_style | py::array::forcecast>> tree_mask,
+         std::optional<f32a> sinks) {
+        if (q.ndim() != 3 || k_cache.ndim() != 4 || v_cache.ndim() != 4 || block_table.ndim() != 2)
+          throw std::invalid_argument("q [N,H,d], caches [pages,kv,ps,d], block_table [N,P]");
+        const bool f16 = k_cache.dtype().is(py::dtype("float16"));
+        if (!f16 && !k_cache.dtype().is(py::dtype::of<float>()))
+          throw std::invalid_argument("KV cache must be float16 or float32");
+        if (!k_cache.dtype().is(v_cache.dtype()))
+          throw std::invalid_argument("K and V caches differ in dtype");
+        if (!(k_cache.flags() & py::array::c_style) || !(v_cache.flags() & py::array::c_style))
+          throw std::invalid_argument("KV caches must be contiguous");
+        AttnArgs a{};
+        a.n_tokens = (int)q.shape(0);
+        a.n_heads = (int)q.shape(1);
+        a.head_dim = (int)q.shape(2);
+        a.n_kv_heads = (int)k_cache.shape(1);
+        a.page_size = (int)k_cache.shape(2);
+        a.max_pages = (int)block_table.shape(1);
+        if (k_cache.shape(3) != a.head_dim || block_table.shape(0) != a.n_tokens ||
+            seq_lens.size() != a.n_tokens)
+          throw std::invalid_argument("shape mismatch");
+        py::array_t<float> out({q.shape(0), q.shape(1), q.shape(2)});
+        a.q = q.data();
+        a.out = out.mutable_data();
+        a.block_table = block_table.data();
+        a.seq_lens = seq_lens.data();
+        a.tree_start = tree_start ? tree_start->data() : nullptr;
+        a.tree_mask = tree_mask ? tree_mask->data() : nullptr;
+        a.sinks = sinks ? sinks->data() : nullptr;
+        a.window = window;
+        a.scale = scale;
+        a.softcap = softcap;
+        const void* kp = k_cache.data();
+        const void* vp = v_cache.data();
+        int rc;
+        {
+          py::gil_scoped_release nogil;
+          rc = cpu_paged_attention(a, kp, vp, f16);
+        }
+        if (rc != 0) throw std::invalid_argument("cpu_paged_attention: bad head counts");
+        return out;
+      },
+      py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
+      py::arg("seq_lens"), py::arg("scale"), py::arg("window") = 0, py::arg("softcap") = 0.f,
+      py::arg("tree_start") = py::none(), py::arg("tree_mask") = py::none(),
+      py::arg("sinks") = py::none(),
+      "paged attention of q [N, H, d] over fp16/fp32 caches [pages, kv, page, d]");
+  m.def(
+      "cpu_silu_mul",
+      [](f32a g, f32a u, float limit, float alpha) {
+        if (g.size() != u.size()) throw std::invalid_argument("g and u differ in size");
+        py::array_t<float> out(std::vector<py::ssize_t>(g.shape(), g.shape() + g.ndim()));
+        const float* gp = g.data();
+        const float* up = u.data();
+        float* op = out.mutable_data();
+        const int64_t n = g.size();
+        {
+          py::gil_scoped_release nogil;
+          cpu_silu_mul(gp, up, op, n, limit, alpha);
+        }
+        return out;
+      },
+      py::arg("g"), py::arg("u"), py::arg("limit") = 0.f, py::arg("alpha") = 1.702f);
+  m.def("exp_approx", [](f32a x) {
+    py::array_t<float> out(std::vector<py::ssize_t>(x.shape(), x.shape() + x.ndim()));
+    for (py::ssize_t i = 0; i < x.size(); ++i) out.mutable_data()[i] = exp_approx(x.data()[i]);
+    return out;
+  });
 
   bind_gguf(m);
   bind_planner(m);

@@ -63,6 +63,9 @@ class EngineConfig:
     draft_model: str = ""
     spec_depth: int = 4
     spec_width: int = 4
+    # CPU device only: dense Q4_K/Q6_K/Q8_0 projections stay quantized and run
+    # through the native int8-dot matmul, attention through the native kernel
+    cpu_native: bool = False
 
 
 @dataclass
@@ -152,7 +155,7 @@ class LLMEngine:
         if dev.type == "cuda":
             model = LlamaGPU(cfg, source, dev, ep=ep, tp=tp)
         else:
-            model = LlamaCPU(cfg, source)
+            model = LlamaCPU(cfg, source, native=ecfg.cpu_native)
         return cls(model, cfg, ecfg, dev)
 
     @classmethod

@@ -599,12 +599,46 @@ def _has_simt(model: LlamaGPU) -> bool:
 
 
 # =========================================================================== CPU
+class _QWeight:
+    """Rows of a GGUF-quantized weight kept in their blocks, multiplied by the
+    native CPU kernel (int8 activations, csrc/native/cpu_qmatmul.cpp)."""
+
+    __slots__ = ("blocks", "qtype", "rows", "K")
+    FORMATS = (Q.Q4_K, Q.Q6_K, Q.Q8_0)
+
+    def __init__(self, blocks, qtype: int, rows: int, K: int):
+        self.blocks = np.ascontiguousarray(blocks.reshape(rows, -1))
+        self.qtype, self.rows, self.K = qtype, rows, K
+
+    def __getitem__(self, sl: slice) -> "_QWeight":
+        part = self.blocks[sl]
+        return _QWeight(part, self.qtype, part.shape[0], self.K)
+
+    @property
+    def shape(self):
+        return (self.rows, self.K)
+
+    def mm(self, x: torch.Tensor) -> torch.Tensor:
+        from .. import _native
+        x2 = x.reshape(-1, self.K).to(torch.float32).contiguous()
+        out = _native.cpu_qmatmul(self.blocks, self.qtype, self.rows, self.K, x2.numpy())
+        return torch.from_numpy(out).reshape(*x.shape[:-1], self.rows).to(x.dtype)
+
+
 class LlamaCPU:
     """fp32 PyTorch implementation on the host: the oracle for the GPU path and
-    the engine backend for CPU-only runs (the two-CPU-peer tiny Llama)."""
+    the engine backend for CPU-only runs (the two-CPU-peer tiny Llama).
+
+    native=True is the optimised CPU inference path: dense Q4_K / Q6_K / Q8_0
+    projections stay in their GGUF blocks and run through the native int8-dot
+    matmul, attention through the native paged kernel (256-key chunks, online
+    softmax) and the SwiGLU tail through the native vector exp; everything else
+    (norms, RoPE, MoE routing, DeltaNet) keeps the fp32 PyTorch code.  The
+    reference's CPU kernels are src/inference/split/attn_rows.rs,
+    prefill_attn.rs and fast_math.rs."""
 
     def __init__(self, cfg: ModelConfig, source, layer_range: tuple[int, int] | None = None,
-                 kv_layer_offset: int | None = None, dtype=torch.float32):
+                 kv_layer_offset: int | None = None, dtype=torch.float32, native: bool = False):
         self.cfg = cfg
         lo, hi = layer_range or (0, cfg.n_layers)
         self.lo, self.hi = lo, hi
@@ -612,10 +646,21 @@ class LlamaCPU:
         # KV caches are stage-local: layer lo of this stage is cache layer 0.
         self.kv_off = 0 if kv_layer_offset is None else kv_layer_offset
         self.dtype = dtype
+        self.native = bool(native) and dtype == torch.float32
         self.nk_loc, self.nv_loc = cfg.ssm_k_heads, cfg.ssm_v_heads
 
         def dq(name):
             t, qt, shape = source.get(name)
+            return torch.from_numpy(Q.dequantize(t.numpy().reshape(-1), qt).reshape(shape)).to(dtype)
+
+        def lw(name):
+            """A dense projection: kept quantized for the native path when its
+            format and width allow, else dequantized."""
+            if not self.native:
+                return dq(name)
+            t, qt, shape = source.get(name)
+            if qt in _QWeight.FORMATS and len(shape) == 2 and shape[1] % 256 == 0:
+                return _QWeight(t.numpy().reshape(-1), qt, shape[0], shape[1])
             return torch.from_numpy(Q.dequantize(t.numpy().reshape(-1), qt).reshape(shape)).to(dtype)
 
         if self.first:
@@ -633,14 +678,14 @@ class LlamaCPU:
                 L.w_in, L.w_z, L.w_ba = dq(b + "attn_qkv.weight"), dq(b + "attn_gate.weight"), dq(b + "ssm_ba.weight")
                 L.conv_w, L.dt_bias, L.A = dq(b + "ssm_conv1d.weight"), dq(b + "ssm_dt.bias"), dq(b + "ssm_a")
                 L.ssm_norm, L.w_out = dq(b + "ssm_norm.weight"), dq(b + "ssm_out.weight")
-                self._load_ffn_cpu(L, b, dq)
+                self._load_ffn_cpu(L, b, dq, lw)
                 self.layers.append(L)
                 continue
             L.kv_idx = n_attn
             n_attn += 1
             qr = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
             if cfg.fused_qkv:
-                wqkv = dq(b + "attn_qkv.weight")
+                wqkv = lw(b + "attn_qkv.weight")
                 L.wq, L.wk, L.wv = wqkv[:qr], wqkv[qr:qr + cfg.kv_dim], wqkv[qr + cfg.kv_dim:]
                 if cfg.attn_bias:
                     bqkv = dq(b + "attn_qkv.bias")
@@ -648,11 +693,11 @@ class LlamaCPU:
                 else:
                     L.bq = L.bk = L.bv = None
             else:
-                L.wq, L.wk, L.wv = dq(b + "attn_q.weight"), dq(b + "attn_k.weight"), dq(b + "attn_v.weight")
+                L.wq, L.wk, L.wv = lw(b + "attn_q.weight"), lw(b + "attn_k.weight"), lw(b + "attn_v.weight")
                 L.bq = dq(b + "attn_q.bias") if cfg.attn_bias else None
                 L.bk = dq(b + "attn_k.bias") if cfg.attn_bias else None
                 L.bv = dq(b + "attn_v.bias") if cfg.attn_bias else None
-            L.wo = dq(b + "attn_output.weight")
+            L.wo = lw(b + "attn_output.weight")
             L.bo = dq(b + "attn_output.bias") if cfg.has_out_bias else None
             L.post_attn = dq(b + "post_attention_norm.weight") if cfg.post_norms else None
             L.post_ffn = dq(b + "post_ffw_norm.weight") if cfg.post_norms else None
@@ -661,12 +706,12 @@ class LlamaCPU:
             L.k_norm = dq(b + "attn_k_norm.weight") if cfg.qk_norm else None
             L.sinks = dq(b + "attn_sinks.weight") if cfg.attn_sinks else None
             L.window = cfg.sliding_window if cfg.is_swa(i) else 0
-            self._load_ffn_cpu(L, b, dq)
+            self._load_ffn_cpu(L, b, dq, lw)
             self.layers.append(L)
         self.n_kv_layers, self.n_lin_layers = n_attn, n_lin
         if self.last:
             self.out_norm = dq("output_norm.weight")
-            self.head = dq("token_embd.weight" if cfg.tie_embeddings else "output.weight")
+            self.head = lw("token_embd.weight" if cfg.tie_embeddings else "output.weight")
         inv, self.attn_factor = rope_inv_freq(cfg)
         self.inv_freq = torch.from_numpy(inv)
         inv_l, self.attn_factor_local = rope_inv_freq(cfg, local=True)
@@ -675,8 +720,9 @@ class LlamaCPU:
 
     linear_state_spec = LlamaGPU.linear_state_spec
 
-    def _load_ffn_cpu(self, L, b, dq):
+    def _load_ffn_cpu(self, L, b, dq, lw=None):
         cfg = self.cfg
+        lw = lw or dq
         L.moe = bool(cfg.n_experts)
         if L.moe:
             gpt = cfg.arch == "gpt-oss"
@@ -693,10 +739,15 @@ class LlamaCPU:
                                                          "ffn_down_shexp.weight"))
                 L.sgi = dq(b + "ffn_gate_inp_shexp.weight")
         elif cfg.fused_gate_up:
-            gu = dq(b + "ffn_up.weight")
-            L.wg, L.wu, L.wd = gu[:cfg.ffn], gu[cfg.ffn:], dq(b + "ffn_down.weight")
+            gu = lw(b + "ffn_up.weight")
+            L.wg, L.wu, L.wd = gu[:cfg.ffn], gu[cfg.ffn:], lw(b + "ffn_down.weight")
         else:
-            L.wg, L.wu, L.wd = dq(b + "ffn_gate.weight"), dq(b + "ffn_up.weight"), dq(b + "ffn_down.weight")
+            L.wg, L.wu, L.wd = lw(b + "ffn_gate.weight"), lw(b + "ffn_up.weight"), lw(b + "ffn_down.weight")
+
+    @staticmethod
+    def _mm(x, W):
+        """x @ W.T for a dense tensor or a quantized weight (native path)."""
+        return W.mm(x) if isinstance(W, _QWeight) else x @ W.T
 
     def _gate_act(self, g):
         if self.cfg.act == "gelu":
@@ -752,15 +803,23 @@ class LlamaCPU:
         u = torch.clamp(u, -cfg.swiglu_limit, cfg.swiglu_limit)
         return g * torch.sigmoid(cfg.swiglu_alpha * g) * (u + 1)
 
+    def _glu(self, g, u):
+        if self.native and self.cfg.act != "gelu":
+            from .. import _native
+            return torch.from_numpy(_native.cpu_silu_mul(g.contiguous().numpy(),
+                                                         u.contiguous().numpy()))
+        return self._gate_act(g) * u
+
     def _ffn(self, L, x, layer: int = -1, b=None):
         if L.moe:
             return self._moe(x, L)
+        mm = self._mm
         if b is None:
-            return (self._gate_act(x @ L.wg.T) * (x @ L.wu.T)) @ L.wd.T
-        gg = self._lora_cpu(layer, "ffn_gate", x, x @ L.wg.T, b)
-        uu = self._lora_cpu(layer, "ffn_up", x, x @ L.wu.T, b)
-        act = self._gate_act(gg) * uu
-        return self._lora_cpu(layer, "ffn_down", act, act @ L.wd.T, b)
+            return mm(self._glu(mm(x, L.wg), mm(x, L.wu)), L.wd)
+        gg = self._lora_cpu(layer, "ffn_gate", x, mm(x, L.wg), b)
+        uu = self._lora_cpu(layer, "ffn_up", x, mm(x, L.wu), b)
+        act = self._glu(gg, uu)
+        return self._lora_cpu(layer, "ffn_down", act, mm(act, L.wd), b)
 
     def _deltanet(self, L, x, b, kv):
         """Gated DeltaNet (sequential recurrence, the definition the GPU
@@ -835,7 +894,6 @@ class LlamaCPU:
         cfg = self.cfg
         N = b.tokens.shape[0]
         nq, nkv, d = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
-        rep = nq // nkv
         h = self.embd[b.tokens.long()].clone() if self.first else h_in.to(self.dtype).clone()
         if self.first and cfg.embed_scale:
             h = h * cfg.embed_scale
@@ -853,9 +911,10 @@ class LlamaCPU:
                 continue
             li = self.kv_off + L.kv_idx
             layer = self.lo + j
-            q = self._lora_cpu(layer, "attn_q", x, x @ L.wq.T, b)
-            k = self._lora_cpu(layer, "attn_k", x, x @ L.wk.T, b)
-            v = self._lora_cpu(layer, "attn_v", x, x @ L.wv.T, b)
+            mm = self._mm
+            q = self._lora_cpu(layer, "attn_q", x, mm(x, L.wq), b)
+            k = self._lora_cpu(layer, "attn_k", x, mm(x, L.wk), b)
+            v = self._lora_cpu(layer, "attn_v", x, mm(x, L.wv), b)
             gate = None
             if cfg.attn_output_gate:
                 qg = q.view(N, nq, 2 * d)
@@ -869,38 +928,14 @@ class LlamaCPU:
             K, V = kv.k(li), kv.v(li)
             K[pages, :, offs, :] = k.to(K.dtype)
             V[pages, :, offs, :] = v.to(V.dtype)
-            att = torch.empty(N, nq, d, dtype=self.dtype)
-            for t in range(N):
-                Lt = int(b.seq_lens[t])
-                lo = max(0, Lt - L.window) if L.window else 0
-                keys = torch.arange(lo, Lt)
-                bt = b.block_table[t].long()
-                kp, ko = bt[keys // ps], keys % ps
-                kk = K[kp, :, ko, :].to(self.dtype)  # [n, nkv, d]
-                vv = V[kp, :, ko, :].to(self.dtype)
-                vis = torch.ones(len(keys), dtype=torch.bool)
-                if b.tree_mask is not None:
-                    ts = int(b.tree_start[t])
-                    m = int(b.tree_mask[t]) & ((1 << 64) - 1)
-                    rel = keys - ts
-                    vis = (rel < 0) | torch.tensor([(rr >= 0 and rr < 64 and (m >> int(rr)) & 1 == 1)
-                                                    for rr in rel.tolist()], dtype=torch.bool)
-                kk = kk.repeat_interleave(rep, dim=1)
-                vv = vv.repeat_interleave(rep, dim=1)
-                s = torch.einsum("hd,nhd->hn", q[t], kk) * self.scale
-                if cfg.attn_softcap:
-                    s = cfg.attn_softcap * torch.tanh(s / cfg.attn_softcap)
-                s = s.masked_fill(~vis[None, :], float("-inf"))
-                if L.sinks is not None:
-                    s = torch.cat([s, L.sinks[:, None]], 1)
-                p = torch.softmax(s, -1)
-                if L.sinks is not None:
-                    p = p[:, :-1]
-                att[t] = torch.einsum("hn,nhd->hd", p, vv)
+            if self.native:
+                att = self._attention_native(L, q, K, V, b)
+            else:
+                att = self._attention(L, q, K, V, b)
             a = att.view(N, nq * d)
             if gate is not None:
                 a = a * gate
-            o = self._lora_cpu(layer, "attn_output", a, a @ L.wo.T, b)
+            o = self._lora_cpu(layer, "attn_output", a, mm(a, L.wo), b)
             if L.bo is not None:
                 o = o + L.bo
             if L.post_attn is not None:
@@ -914,7 +949,57 @@ class LlamaCPU:
         if not self.last:
             return h
         x = self._norm(h[b.sample_rows.long()], self.out_norm)
-        logits = x @ self.head.T
+        logits = self._mm(x, self.head)
         if cfg.final_softcap:
             logits = cfg.final_softcap * torch.tanh(logits / cfg.final_softcap)
         return logits
+
+    def _attention(self, L, q, K, V, b):
+        """The fp32 oracle: per row, gather its keys and take a plain softmax."""
+        cfg = self.cfg
+        N, nq, d = q.shape
+        rep = nq // K.shape[1]
+        ps = K.shape[2]
+        att = torch.empty(N, nq, d, dtype=self.dtype)
+        for t in range(N):
+            Lt = int(b.seq_lens[t])
+            lo = max(0, Lt - L.window) if L.window else 0
+            keys = torch.arange(lo, Lt)
+            bt = b.block_table[t].long()
+            kp, ko = bt[keys // ps], keys % ps
+            kk = K[kp, :, ko, :].to(self.dtype)  # [n, nkv, d]
+            vv = V[kp, :, ko, :].to(self.dtype)
+            vis = torch.ones(len(keys), dtype=torch.bool)
+            if b.tree_mask is not None:
+                ts = int(b.tree_start[t])
+                m = int(b.tree_mask[t]) & ((1 << 64) - 1)
+                rel = keys - ts
+                vis = (rel < 0) | torch.tensor([(rr >= 0 and rr < 64 and (m >> int(rr)) & 1 == 1)
+                                                for rr in rel.tolist()], dtype=torch.bool)
+            kk = kk.repeat_interleave(rep, dim=1)
+            vv = vv.repeat_interleave(rep, dim=1)
+            s = torch.einsum("hd,nhd->hn", q[t], kk) * self.scale
+            if cfg.attn_softcap:
+                s = cfg.attn_softcap * torch.tanh(s / cfg.attn_softcap)
+            s = s.masked_fill(~vis[None, :], float("-inf"))
+            if L.sinks is not None:
+                s = torch.cat([s, L.sinks[:, None]], 1)
+            p = torch.softmax(s, -1)
+            if L.sinks is not None:
+                p = p[:, :-1]
+            att[t] = torch.einsum("hn,nhd->hd", p, vv)
+        return att
+
+    def _attention_native(self, L, q, K, V, b):
+        from .. import _native
+        opt = {}
+        if b.tree_mask is not None:
+            opt["tree_start"] = b.tree_start.numpy()
+            opt["tree_mask"] = b.tree_mask.numpy()
+        if L.sinks is not None:
+            opt["sinks"] = L.sinks.float().numpy()
+        out = _native.cpu_paged_attention(
+            q.to(torch.float32).contiguous().numpy(), K.numpy(), V.numpy(),
+            b.block_table.numpy(), b.seq_lens.numpy(), float(self.scale), window=int(L.window),
+            softcap=float(self.cfg.attn_softcap or 0.0), **opt)
+        return torch.from_numpy(out).to(self.dtype)

@@ -15,9 +15,12 @@ overrides.  Names kept where the meaning matches:
                                      preset name, "self" or "ngram")
   speculative_gamma = 4           -> EngineConfig.spec_depth (draft tree depth)
   speculative_width = 4           -> EngineConfig.spec_width (children kept per level)
+  cpu_native = false              -> EngineConfig.cpu_native (CPU device: quantized weights
+                                     through the native int8 matmul and paged attention)
 
 Environment: SWARMLLM_MAX_MODEL_LEN, SWARMLLM_MAX_RUNNING, SWARMLLM_PREFILL_CHUNK,
-SWARMLLM_KV_PAGES, SWARMLLM_KV_FRACTION, SWARMLLM_PREFIX_CACHE, SWARMLLM_CUDA_GRAPH.
+SWARMLLM_KV_PAGES, SWARMLLM_KV_FRACTION, SWARMLLM_PREFIX_CACHE, SWARMLLM_CUDA_GRAPH,
+SWARMLLM_CPU_NATIVE.
 
 A [server] table (rpm, cors_origins, max_body) holds the request-guard
 settings; the admin API re-reads it on /api/admin/config/reload.
@@ -45,6 +48,7 @@ _TOML_KEYS = {
     "draft_model_path": "draft_model",      # drafter GGUF (or preset / "self" / "ngram")
     "speculative_gamma": "spec_depth",      # draft depth (tokens guessed per round)
     "speculative_width": "spec_width",
+    "cpu_native": "cpu_native",
 }
 
 _ENV = {
@@ -59,6 +63,7 @@ _ENV = {
     "SWARMLLM_DRAFT_MODEL": ("draft_model", str),
     "SWARMLLM_SPEC_DEPTH": ("spec_depth", int),
     "SWARMLLM_SPEC_WIDTH": ("spec_width", int),
+    "SWARMLLM_CPU_NATIVE": ("cpu_native", lambda v: v not in ("0", "false", "False")),
 }
 
 
