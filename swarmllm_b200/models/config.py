@@ -12,6 +12,11 @@ mapping in ``src/inference/split/loader/mod.rs``):
 * ``qwen3next`` hybrid: gated DeltaNet linear-attention layers and gated full
                 attention layers (3:1), q/k RMSNorm, partial NEOX RoPE,
                 512-expert MoE with a shared expert.
+* ``qwen35`` / ``qwen35moe``  Qwen 3.5: the same hybrid layers with a dense
+                SwiGLU FFN (``qwen35``) or routed experts plus a shared expert
+                (``qwen35moe``); its files tile the value heads over the key
+                heads and keep beta and alpha apart, which the loader puts in
+                the kernels' order (models/layout.py).
 
 The other families are the dense / MoE decoder with options, read from the
 GGUF architecture name (llama.cpp's names and metadata keys):
@@ -312,7 +317,7 @@ def preset(name: str) -> ModelConfig:
 
 # --------------------------------------------------------------------------- GGUF mapping
 _FAMILIES = ("llama", "mistral", "qwen2", "qwen3", "qwen2moe", "qwen3moe", "gemma", "gemma2",
-             "gemma3", "phi3", "glm4", "gpt-oss", "qwen3next")
+             "gemma3", "phi3", "glm4", "gpt-oss", "qwen3next", "qwen35", "qwen35moe")
 _ARCH_KEYS = {f: f for f in _FAMILIES}    # GGUF general.architecture == family name
 
 
@@ -345,7 +350,7 @@ def apply_family(cfg: ModelConfig, md: dict | None = None) -> ModelConfig:
     if fam == "gpt-oss":
         cfg.rope_neox, cfg.attn_sinks, cfg.attn_bias, cfg.swa_every = True, True, True, 2
         cfg.swiglu_limit = cfg.swiglu_limit or 7.0
-    if fam == "qwen3next":
+    if fam in ("qwen3next", "qwen35", "qwen35moe"):
         cfg.rope_neox, cfg.qk_norm, cfg.attn_output_gate = True, True, True
     return cfg
 
@@ -390,6 +395,7 @@ def to_gguf_metadata(cfg: ModelConfig) -> dict:
         md[f"{a}.ssm.group_count"] = cfg.ssm_k_heads
         md[f"{a}.ssm.time_step_rank"] = cfg.ssm_v_heads
         md[f"{a}.ssm.state_size"] = cfg.ssm_head_dim
+        md[f"{a}.ssm.inner_size"] = cfg.ssm_v_heads * cfg.ssm_head_dim
     # Engine-specific keys (prefixed) carry what GGUF has no standard key for.
     md["swarmllm.config"] = __import__("json").dumps(cfg.to_dict())
     return md
@@ -432,9 +438,17 @@ def from_gguf_metadata(md: dict) -> ModelConfig:
             cfg.rope_scaling["attn_factor"] = g("rope.scaling.attn_factor")
     if g("attention.scale"):
         cfg.attn_scale = float(g("attention.scale"))
-    if fam == "qwen3next":
+    if fam in ("qwen3next", "qwen35", "qwen35moe"):
+        # llama.cpp's keys: group_count = key heads, time_step_rank = value
+        # heads, state_size = key head width, inner_size = value heads x width
         cfg.full_attn_interval = g("full_attention_interval", 4)
         cfg.ssm_conv_kernel = g("ssm.conv_kernel", 4)
+        cfg.ssm_k_heads = g("ssm.group_count", cfg.ssm_k_heads)
+        cfg.ssm_v_heads = g("ssm.time_step_rank", cfg.ssm_v_heads)
+        cfg.ssm_head_dim = g("ssm.state_size", cfg.ssm_head_dim)
+        inner = g("ssm.inner_size")
+        if inner and cfg.ssm_v_heads and inner != cfg.ssm_v_heads * cfg.ssm_head_dim:
+            raise ValueError("DeltaNet value heads wider than key heads are not supported")
     if fam in ("gemma", "gemma2", "gemma3") and not g("vocab_size"):
         cfg.vocab = len(md.get("tokenizer.ggml.tokens", [])) or cfg.vocab
     return apply_family(cfg, md)

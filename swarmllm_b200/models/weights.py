@@ -21,6 +21,7 @@ import torch
 from ..gguf import quants as Q
 from ..gguf.file import GGUFReader, GGUFWriter, ShardedGguf
 from .config import ModelConfig, from_gguf_metadata, to_gguf_metadata
+from .layout import HYBRID_FAMILIES, file_specs, kernel_name, to_file, to_kernel
 
 
 def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
@@ -147,15 +148,23 @@ class GgufSource:
                 self.cfg.rope_factors = Q.dequantize(t.numpy().reshape(-1), qt).tolist()
 
     def has(self, name: str) -> bool:
-        return name in self.f.tensors
+        return all(n in self.f.tensors for n in kernel_name(self.cfg.arch, name))
+
+    def _raw(self, name: str):
+        ti = self.f.tensors[name]
+        return np.array(self.f.tensor_bytes(name), copy=True).reshape(-1), ti.qtype, ti.shape
 
     def get(self, name: str, device=None):
-        ti = self.f.tensors[name]
-        b = self.f.tensor_bytes(name)
-        t = torch.from_numpy(np.array(b, copy=True))
+        """A tensor as (bytes, qtype, shape), in the kernels' order: the hybrid
+        families' DeltaNet tensors are reordered from the file's (layout.py)."""
+        if self.cfg.arch in HYBRID_FAMILIES:
+            raw, qt, shape = to_kernel(self.cfg, name, self._raw)
+        else:
+            raw, qt, shape = self._raw(name)
+        t = torch.from_numpy(np.ascontiguousarray(raw))
         if device is not None:
             t = t.to(device)
-        return t, ti.qtype, ti.shape
+        return t, qt, shape
 
 
 class RandomSource:
@@ -254,8 +263,8 @@ def write_random_gguf(cfg: ModelConfig, path: str, seed: int = 0, std: float = 0
     w = GGUFWriter(cfg.arch)
     for k, v in to_gguf_metadata(cfg).items():
         w.add(k, v)
-    for name, shape, qt in tensor_specs(cfg):
-        t, _, _ = src.get(name)
-        w.add_tensor(name, t.numpy(), qt, shape)
+    for name, shape, qt in file_specs(cfg, tensor_specs(cfg)):
+        data = to_file(cfg, name, shape, qt, lambda n: src.get(n)[0].numpy())
+        w.add_tensor(name, data, qt, shape)
     w.write(path)
     return path

@@ -17,7 +17,15 @@ BUILTIN = {
     # harmony (gpt-oss): final channel only
     "gpt-oss": ("{% for m in messages %}<|start|>{{ m['role'] }}<|message|>{{ m['content'] }}<|end|>"
                 "{% endfor %}{% if add_generation_prompt %}<|start|>assistant<|channel|>final<|message|>{% endif %}"),
+    # Gemma turns (no system role: a system message is sent as a user turn)
+    "gemma": ("{% for m in messages %}<start_of_turn>{{ 'model' if m['role'] == 'assistant' else 'user' }}\n"
+              "{{ m['content'] }}<end_of_turn>\n{% endfor %}"
+              "{% if add_generation_prompt %}<start_of_turn>model\n{% endif %}"),
 }
+for _fam in ("qwen2", "qwen3", "qwen2moe", "qwen3moe", "qwen35", "qwen35moe"):
+    BUILTIN[_fam] = BUILTIN["qwen3next"]
+for _fam in ("gemma2", "gemma3"):
+    BUILTIN[_fam] = BUILTIN["gemma"]
 
 
 def render(messages: list[dict], arch: str = "llama", template: str | None = None,
