@@ -5,10 +5,12 @@ that the request's `response_format` json_schema accepts.
 every value is checked against the schema that applies at its place: the
 allowed types, object keys (`properties`, `required`, `additionalProperties`),
 array items and item counts (`items`, `minItems`, `maxItems`), `enum` /
-`const` values, integers versus numbers, and `anyOf` / `oneOf` alternatives.
-It is a set of deterministic parsers, one per alternative still open: a
-character is accepted if at least one parser takes it.  Keywords outside that
-list (string patterns, numeric ranges, formats) are not enforced.  A parser
+`const` values, integers versus numbers, string `pattern`s (regex_guard.py:
+the ECMA subset without back-references or look-around), the fixed-shape
+`format`s (date, time, date-time, uuid, ipv4, email), `minLength` /
+`maxLength`, and `anyOf` / `oneOf` alternatives.  It is a set of
+deterministic parsers, one per alternative still open: a character is
+accepted if at least one parser takes it.  Numeric ranges are not enforced.  A parser
 never takes a character after which the value could not be completed (a ','
 with no unseen allowed key left, a '}' with a required key missing, a ']' short
 of minItems), so decoding cannot paint itself into a corner.  Whitespace
@@ -22,6 +24,8 @@ schema (src/inference/reply_grammar.rs:90,156).
 from __future__ import annotations
 
 import json
+
+from .regex_guard import FORMAT_PATTERNS, compile_pattern
 
 _WS = " \t\n\r"
 _DIGITS = "0123456789"
@@ -137,7 +141,7 @@ class _Parser:
     """One deterministic parse under one choice of anyOf / oneOf alternatives."""
 
     __slots__ = ("stack", "exp", "tok", "key", "uni", "num", "integer", "lit", "lpos",
-                 "cands", "text", "pending", "ws", "nl")
+                 "cands", "text", "pending", "ws", "nl", "scon", "sst", "slen", "uhex")
 
     def __init__(self):
         self.stack: list = []
@@ -153,12 +157,16 @@ class _Parser:
         self.pending: dict = {}        # schema of the next value to start
         self.ws = 0                    # blanks read since the last token
         self.nl = False                # ... the first of them a newline
+        self.scon = None               # _StrRule of the string being read, if any
+        self.sst = None                # its patterns' NFA state sets
+        self.slen = 0                  # characters of the string so far
+        self.uhex = ""                 # hex digits of a \u escape
 
     def copy(self) -> "_Parser":
         c = _Parser.__new__(_Parser)
         c.stack = [f.copy() for f in self.stack]
         for f in ("exp", "tok", "key", "uni", "num", "integer", "lit", "lpos", "text",
-                  "pending", "ws", "nl"):
+                  "pending", "ws", "nl", "scon", "sst", "slen", "uhex"):
             setattr(c, f, getattr(self, f))
         c.cands = list(self.cands)
         return c
@@ -208,6 +216,9 @@ class _Parser:
             return True
         if c == '"' and ok("string"):
             self.tok, self.key = _STR, False
+            self.scon = _StrRule.of(schema)
+            self.slen = 0
+            self.sst = self.scon.start() if self.scon is not None else None
             return True
         if (c == "-" or c in _DIGITS) and (ok("number") or ok("integer")):
             self.tok = _NUM
@@ -241,18 +252,20 @@ class _Parser:
             return self._str_char(c)
         if t == _ESC:
             if c == "u":
-                self.tok, self.uni = _UNI, 4
-            elif c in '"\\/bfnrt':
+                self.tok, self.uni, self.uhex = _UNI, 4, ""
+                return True
+            if c in '"\\/bfnrt':
                 self.tok = _STR
-            else:
-                return False
-            return True
+                return self._str_value_char(_JSON_ESC[c])
+            return False
         if t == _UNI:
             if c not in "0123456789abcdefABCDEF":
                 return False
             self.uni -= 1
+            self.uhex += c
             if self.uni == 0:
                 self.tok = _STR
+                return self._str_value_char(chr(int(self.uhex, 16)))
             return True
         if t == _LIT:
             if c != self.lit[self.lpos]:
@@ -368,13 +381,80 @@ class _Parser:
             top.key += c
             return True
         if c == '"':
+            if self.scon is not None and not self.scon.complete(self.sst, self.slen):
+                return False
             self.tok = _NONE
+            self.scon = self.sst = None
             self._end_value()
         elif c == "\\":
+            if self.scon is not None and self.escapes_blocked():
+                return False
             self.tok = _ESC
         elif ord(c) < 0x20:
             return False
+        else:
+            return self._str_value_char(c)
         return True
+
+    def escapes_blocked(self) -> bool:
+        """No escape can start when the string is already at maxLength."""
+        return self.scon.max_len is not None and self.slen >= self.scon.max_len
+
+    def _str_value_char(self, ch: str) -> bool:
+        """One decoded character of a string value, against its rules."""
+        if self.scon is None:
+            return True
+        r = self.scon
+        if r.max_len is not None and self.slen >= r.max_len:
+            return False
+        nxt = r.step(self.sst, ch)
+        if nxt is None:
+            return False
+        self.sst, self.slen = nxt, self.slen + 1
+        return True
+
+
+_JSON_ESC = {'"': '"', "\\": "\\", "/": "/", "b": "\b", "f": "\f", "n": "\n", "r": "\r",
+             "t": "\t"}
+
+
+class _StrRule:
+    """The constraints on one string value: patterns (`pattern` and a
+    fixed-shape `format`, all of which must match) and the length bounds."""
+
+    __slots__ = ("pats", "min_len", "max_len")
+
+    @staticmethod
+    def of(schema: dict) -> "_StrRule | None":
+        pats = []
+        for src in (schema.get("pattern"), FORMAT_PATTERNS.get(schema.get("format"))):
+            if isinstance(src, str):
+                p = compile_pattern(src)
+                if p is not None:
+                    pats.append(p)
+        mn, mx = schema.get("minLength"), schema.get("maxLength")
+        mn = mn if isinstance(mn, int) and mn > 0 else 0
+        mx = mx if isinstance(mx, int) and mx >= 0 else None
+        if not pats and not mn and mx is None:
+            return None
+        r = _StrRule()
+        r.pats, r.min_len, r.max_len = tuple(pats), mn, mx
+        return r
+
+    def start(self):
+        return tuple(p.start() for p in self.pats)
+
+    def step(self, states, ch: str):
+        out = []
+        for p, st in zip(self.pats, states):
+            n = p.step(st, ch)
+            if not n:
+                return None
+            out.append(n)
+        return tuple(out)
+
+    def complete(self, states, n: int) -> bool:
+        return n >= self.min_len and all(p.accepts(st) for p, st in zip(self.pats, states))
 
 
 class SchemaPrefix:

@@ -94,3 +94,67 @@ def test_constrained_api_output_matches_schema():
                     assert set(v) == {"ok", "n"} and isinstance(v["ok"], bool) and v["n"] in (1, 2, 3)
     finally:
         ae.shutdown()
+
+
+def test_regex_subset_matches_python_re():
+    """The pattern NFA agrees with Python's re (fullmatch semantics via \\Z)
+    on random strings, for anchored and unanchored patterns."""
+    import random
+    import re
+    from swarmllm_b200.serve.regex_guard import FORMAT_PATTERNS, compile_pattern
+    cases = [r"^\d{3}-\d{4}$", r"^[A-Z][a-z]+( [A-Z][a-z]+)*$", r"ab|cd", r"^(?:foo|bar)+baz?$",
+             r"^[^@\s]+@[^@\s]+\.[a-z]{2,6}$", r"^x{2,4}y{0,}z?$", r"^[-+]?\d*\.?\d+$",
+             r"colou?r", r"^\w+\s\w+$", r"^a.c$", r"^[\]a-]+$", r"^a{3}$"] + \
+        list(FORMAT_PATTERNS.values())
+    rng = random.Random(0)
+    alphabet = "abcdxyzABZ0123456789-+.@ _:TZ]\n"
+    for c in cases:
+        p = compile_pattern(c)
+        assert p is not None, c
+        rx = re.compile(c[:-1] + r"\Z" if c.endswith("$") else c)
+        for _ in range(1500):
+            s = "".join(rng.choice(alphabet) for _ in range(rng.randint(0, 12)))
+            assert p.fullmatch(s) == (rx.search(s) is not None), (c, s)
+    for c in (r"(?=a)b", r"(a)\1", r"a^b", r"(ab", r"\bfoo"):
+        assert compile_pattern(c) is None, c       # outside the subset: not enforced
+
+
+def test_string_pattern_format_and_length():
+    sch = {"type": "object", "properties": {
+        "zip": {"type": "string", "pattern": "^[0-9]{5}$"},
+        "day": {"type": "string", "format": "date"},
+        "nick": {"type": "string", "minLength": 2, "maxLength": 3}},
+        "required": ["zip"]}
+    assert _ok(sch, '{"zip":"12345"}', done=True)
+    assert not _ok(sch, '{"zip":"1234a')
+    assert not _ok(sch, '{"zip":"1234"')              # closing quote before 5 digits
+    assert not _ok(sch, '{"zip":"123456')
+    assert _ok(sch, '{"zip":"00000","day":"2024-02-29"}', done=True)
+    assert not _ok(sch, '{"zip":"00000","day":"2024-13')
+    assert _ok(sch, '{"zip":"00000","nick":"ab"}', done=True)
+    assert not _ok(sch, '{"zip":"00000","nick":"a"')
+    assert not _ok(sch, '{"zip":"00000","nick":"abcd')
+    # escapes count as the character they stand for
+    assert _ok({"type": "string", "pattern": "^a\\nb$"}, '"a\\nb"', done=True)
+    assert _ok({"type": "string", "pattern": "^\\u00e9$"}, '"\\u00e9"', done=True)
+    assert not _ok({"type": "string", "maxLength": 1}, '"a\\')
+
+
+def test_constrained_random_walk_respects_pattern():
+    """Drawing characters at random among those the recogniser allows always
+    ends in a string the pattern fully matches."""
+    import random
+    import re
+    sch = {"type": "string", "pattern": "^(ab|c)+-[0-9]{2,3}$"}
+    rng = random.Random(3)
+    alphabet = list('abc-0123456789"x')
+    for _ in range(30):
+        s, text = SchemaPrefix(sch), ""
+        while not s.done:
+            allowed = [c for c in alphabet if s.copy().feed(c)]
+            assert allowed, text
+            c = rng.choice(allowed)
+            assert s.feed(c)
+            text += c
+            assert len(text) < 200
+        assert re.fullmatch("(ab|c)+-[0-9]{2,3}", json.loads(text))
