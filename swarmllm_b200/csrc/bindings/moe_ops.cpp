@@ -3,15 +3,20 @@
 
 namespace {
 
-void moe_topk(const GemmResult& lg, OptT br, int64_t T, int64_t E, int64_t k,
-              bool softmax_after_topk, Tensor ids, Tensor wts, Tensor counts) {
+void moe_topk(const GemmResult& lg, OptT br, int64_t T, int64_t E, int64_t k, int64_t mode,
+              OptT sel_b, bool norm, double scale, Tensor ids, Tensor wts, Tensor counts) {
   CHECK_DT(ids, at::kInt); CHECK_DT(wts, at::kFloat); CHECK_DT(counts, at::kInt);
   TORCH_CHECK(lg.g.rows == E && lg.g.T >= T, "router logits shape");
   TORCH_CHECK(ids.numel() >= T * k && wts.numel() >= T * k, "ids/wts too small");
+  if (sel_b.has_value()) {
+    CHECK_DT((*sel_b), at::kFloat);
+    TORCH_CHECK(sel_b->numel() >= E, "selection bias too small");
+  }
   const at::cuda::CUDAGuard guard(ids.device());
-  int rc = launch_moe_topk(lg.g, ptr_or_null<float>(br), (int)T, (int)E, (int)k,
-                           softmax_after_topk ? 1 : 0, ids.data_ptr<int32_t>(),
-                           wts.data_ptr<float>(), counts.data_ptr<int>(), cur_stream());
+  int rc = launch_moe_topk(lg.g, ptr_or_null<float>(br), (int)T, (int)E, (int)k, (int)mode,
+                           ptr_or_null<float>(sel_b), norm ? 1 : 0, (float)scale,
+                           ids.data_ptr<int32_t>(), wts.data_ptr<float>(),
+                           counts.data_ptr<int>(), cur_stream());
   TORCH_CHECK(rc == 0, "moe_topk failed: rc=", rc);
 }
 

@@ -124,8 +124,11 @@ int moe_tok_tile(int pairs, int n_experts);
 int moe_max_tiles(int pairs, int n_experts, int tok_tile);
 long long moe_packed_bytes(int fmt, int rows, int K);
 int launch_mxfp4_repack(const void* src, int rows, int K, void* dst, cudaStream_t s);
-int launch_moe_topk(const swarm::GemmOut& lg, const float* br, int T, int E, int k,
-                    int softmax_after_topk, int32_t* ids, float* wts, int* counts, cudaStream_t s);
+// mode 0 softmax over all, 1 top-k then softmax, 2 sigmoid scores with a
+// selection bias (sel_b, may be null), optional renormalisation and a scale
+int launch_moe_topk(const swarm::GemmOut& lg, const float* br, int T, int E, int k, int mode,
+                    const float* sel_b, int norm, float scale, int32_t* ids, float* wts,
+                    int* counts, cudaStream_t s);
 int launch_moe_plan(int* counts, int E, int tok_tile, int* offsets, int* cursor, void* tiles,
                     int* n_tiles, int max_tiles, int* status, cudaStream_t s);
 int launch_moe_scatter(const __half* x, int x_stride, int H, const int32_t* ids, int P, int k,

@@ -50,8 +50,15 @@ constexpr int kMxUnitBytes = 128 * kMxRowBytes;  // 17408
 // token: all threads read the (split-K) logits in parallel into shared
 // memory, then warp 0 adds nothing more than the selection: top-k (ties ->
 // lower expert id), routing weights, per-expert token counts.
+// mode 0: softmax over all experts, weights = their probabilities;
+// mode 1: top-k on the logits, softmax over the k selected;
+// mode 2 (GLM-4.5 / DeepSeek-V3 style): scores sigmoid(logit), top-k on
+//   score + sel_b[e] (a selection bias that does not enter the weight),
+//   weights = the k scores, divided by their sum when `norm`, times `scale`.
 __global__ void __launch_bounds__(256) moe_topk_kernel(GemmOut lg, const float* __restrict__ br,
-                                                       int T, int E, int k, int softmax_after_topk,
+                                                       int T, int E, int k, int mode,
+                                                       const float* __restrict__ sel_b, int norm,
+                                                       float scale,
                                                        int32_t* __restrict__ ids,
                                                        float* __restrict__ wts,
                                                        int* __restrict__ counts) {
@@ -62,11 +69,14 @@ __global__ void __launch_bounds__(256) moe_topk_kernel(GemmOut lg, const float* 
   if (threadIdx.x >= 32) return;
   const int lane = threadIdx.x;
   constexpr int kMaxPer = 16;  // E <= 512
+  const bool sig = mode == 2;
+  const int softmax_after_topk = mode == 1;
   float v[kMaxPer];
 #pragma unroll
   for (int i = 0; i < kMaxPer; ++i) {
     const int e = lane + 32 * i;
-    v[i] = e < E ? lgs[e] : -INFINITY;
+    v[i] = e < E ? (sig ? 1.f / (1.f + __expf(-lgs[e])) + (sel_b ? sel_b[e] : 0.f) : lgs[e])
+                 : -INFINITY;
   }
   float sel_v = 0.f, top = 0.f, denom_all = 0.f;
   int sel_e = 0;
@@ -82,7 +92,7 @@ __global__ void __launch_bounds__(256) moe_topk_kernel(GemmOut lg, const float* 
       const int oe = __shfl_xor_sync(0xffffffffu, be, o);
       if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
     }
-    if (j == 0) {
+    if (j == 0 && !sig) {
       top = bv;
       if (!softmax_after_topk) {  // softmax over all experts, then pick
         float sum = 0.f;
@@ -100,12 +110,20 @@ __global__ void __launch_bounds__(256) moe_topk_kernel(GemmOut lg, const float* 
         if (lane + 32 * i == be) v[i] = -INFINITY;
     }
   }
-  const float ex = lane < k ? __expf(sel_v - top) : 0.f;
-  const float denom = softmax_after_topk ? warp_sum(ex) : denom_all;
+  float w;
+  if (sig) {  // the selected expert's score without the selection bias
+    const float sc = lane < k ? 1.f / (1.f + __expf(-lgs[sel_e])) : 0.f;
+    const float sum = warp_sum(sc);
+    w = (norm && sum > 0.f ? sc / sum : sc) * scale;
+  } else {
+    const float ex = lane < k ? __expf(sel_v - top) : 0.f;
+    const float denom = softmax_after_topk ? warp_sum(ex) : denom_all;
+    w = ex / denom;
+  }
   if (lane < k) {
     const size_t o = (size_t)t * k + lane;
     ids[o] = sel_e;
-    wts[o] = ex / denom;
+    wts[o] = w;
     atomicAdd(&counts[sel_e], 1);
   }
 }
@@ -668,11 +686,12 @@ int launch_mxfp4_repack(const void* src, int rows, int K, void* dst, cudaStream_
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -2;
 }
 
-int launch_moe_topk(const GemmOut& lg, const float* br, int T, int E, int k,
-                    int softmax_after_topk, int32_t* ids, float* wts, int* counts, cudaStream_t s) {
+int launch_moe_topk(const GemmOut& lg, const float* br, int T, int E, int k, int mode,
+                    const float* sel_b, int norm, float scale, int32_t* ids, float* wts,
+                    int* counts, cudaStream_t s) {
   if (T <= 0) return 0;
-  if (E > 512 || k > 32 || k > E) return -1;
-  moe_topk_kernel<<<T, 256, 0, s>>>(lg, br, T, E, k, softmax_after_topk, ids, wts, counts);
+  if (E > 512 || k > 32 || k > E || mode < 0 || mode > 2) return -1;
+  moe_topk_kernel<<<T, 256, 0, s>>>(lg, br, T, E, k, mode, sel_b, norm, scale, ids, wts, counts);
   return cudaPeekAtLastError() == cudaSuccess ? 0 : -4;
 }
 

@@ -39,6 +39,12 @@ GGUF architecture name (llama.cpp's names and metadata keys):
                 LongRoPE per-dimension factors.
 * ``glm4``      fused q|k|v with biases, fused gate|up, partial interleaved
                 RoPE, post-attention / post-FFN norms.
+* ``glm4moe``   GLM-4.5: q/k/v with biases, partial NEOX RoPE, optional q/k
+                norms, leading dense layers, then sigmoid-scored experts chosen
+                with a selection bias (``exp_probs_b``), renormalised and
+                scaled, plus an ungated shared expert; the file's
+                ``post_attention_norm`` is the norm before the FFN; the
+                trailing next-token-prediction blocks are not run.
 """
 from __future__ import annotations
 
@@ -89,6 +95,11 @@ class ModelConfig:
     expert_ffn: int = 0
     shared_expert_ffn: int = 0
     moe_softmax_after_topk: bool = True  # gpt-oss: softmax over the selected logits
+    moe_gating: str = "softmax"         # "sigmoid": GLM-4.5 scores with a selection bias
+    moe_norm_topk: bool = True          # sigmoid gating: weights divided by their sum
+    moe_scale: float = 1.0              # sigmoid gating: routed-weight multiplier
+    moe_dense_layers: int = 0           # leading layers with a dense FFN (size `ffn`)
+    shared_expert_gated: bool = True    # a sigmoid gate (ffn_gate_inp_shexp) on the shared expert
     swiglu_limit: float = 0.0           # gpt-oss clamped SwiGLU (7.0)
     swiglu_alpha: float = 1.702
     # hybrid linear attention (gated DeltaNet)
@@ -149,6 +160,17 @@ class ModelConfig:
         if name in ("attn_v.weight", "ffn_down.weight") and self.more_bits_layer(layer):
             return "Q6_K"
         return None
+
+    def is_moe_layer(self, layer: int) -> bool:
+        return bool(self.n_experts) and layer >= self.moe_dense_layers
+
+    @property
+    def moe_mode(self) -> int:
+        """Routing mode of the top-k kernel: 0 softmax over all experts, 1
+        top-k then softmax, 2 sigmoid scores with a selection bias."""
+        if self.moe_gating == "sigmoid":
+            return 2
+        return 1 if self.moe_softmax_after_topk else 0
 
     def is_linear_attn(self, layer: int) -> bool:
         return bool(self.full_attn_interval) and (layer + 1) % self.full_attn_interval != 0
@@ -317,7 +339,7 @@ def preset(name: str) -> ModelConfig:
 
 # --------------------------------------------------------------------------- GGUF mapping
 _FAMILIES = ("llama", "mistral", "qwen2", "qwen3", "qwen2moe", "qwen3moe", "gemma", "gemma2",
-             "gemma3", "phi3", "glm4", "gpt-oss", "qwen3next", "qwen35", "qwen35moe")
+             "gemma3", "phi3", "glm4", "glm4moe", "gpt-oss", "qwen3next", "qwen35", "qwen35moe")
 _ARCH_KEYS = {f: f for f in _FAMILIES}    # GGUF general.architecture == family name
 
 
@@ -347,6 +369,18 @@ def apply_family(cfg: ModelConfig, md: dict | None = None) -> ModelConfig:
         cfg.fused_qkv, cfg.fused_gate_up, cfg.post_norms = True, True, True
         cfg.attn_bias, cfg.attn_out_bias = True, False
         cfg.rope_dim = cfg.rope_dim or cfg.head_dim // 2
+    if fam == "glm4moe":
+        cfg.rope_neox, cfg.attn_bias, cfg.attn_out_bias = True, True, False
+        cfg.rope_dim = cfg.rope_dim or cfg.head_dim // 2
+        cfg.moe_gating, cfg.shared_expert_gated = "sigmoid", False
+        if md is not None:
+            cfg.moe_dense_layers = int(g("leading_dense_block_count", cfg.moe_dense_layers))
+            cfg.moe_scale = float(g("expert_weights_scale", cfg.moe_scale))
+            cfg.moe_norm_topk = bool(g("expert_weights_norm", cfg.moe_norm_topk))
+            n_sh = int(g("expert_shared_count", 1 if cfg.shared_expert_ffn else 0))
+            cfg.shared_expert_ffn = n_sh * cfg.expert_ffn if n_sh else 0
+            # next-token-prediction blocks follow the model's own layers
+            cfg.n_layers -= int(g("nextn_predict_layers", 0))
     if fam == "gpt-oss":
         cfg.rope_neox, cfg.attn_sinks, cfg.attn_bias, cfg.swa_every = True, True, True, 2
         cfg.swiglu_limit = cfg.swiglu_limit or 7.0
@@ -383,6 +417,13 @@ def to_gguf_metadata(cfg: ModelConfig) -> dict:
         md[f"{a}.expert_feed_forward_length"] = cfg.expert_ffn
         if cfg.shared_expert_ffn:
             md[f"{a}.expert_shared_feed_forward_length"] = cfg.shared_expert_ffn
+        if cfg.moe_gating == "sigmoid":
+            md[f"{a}.expert_gating_func"] = 2
+            md[f"{a}.expert_weights_scale"] = float(cfg.moe_scale)
+            md[f"{a}.expert_weights_norm"] = bool(cfg.moe_norm_topk)
+            md[f"{a}.expert_shared_count"] = cfg.shared_expert_ffn // max(1, cfg.expert_ffn)
+        if cfg.moe_dense_layers:
+            md[f"{a}.leading_dense_block_count"] = cfg.moe_dense_layers
     if cfg.sliding_window:
         md[f"{a}.attention.sliding_window"] = cfg.sliding_window
     if cfg.attn_softcap:

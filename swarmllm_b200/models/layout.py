@@ -13,6 +13,10 @@ as the reference reads them in src/inference/layers/qwen35.rs:116-230):
   f % n_k -- and separate ``ssm_beta`` / ``ssm_alpha`` tensors.  Kernel head
   g = kh * r + j is file head j * n_k + kh.
 
+GLM-4.5 (``glm4moe``) files name the norm before the feed-forward
+``post_attention_norm``; the engine calls it ``ffn_norm`` like every other
+family's, so it is renamed on the way in and out.
+
 ``to_kernel`` turns a file tensor into the kernels' order when a GGUF is read
 (whole rows move, still quantized; ``ssm_out``'s value heads are columns,
 moved as whole blocks where a block fits in a head, else the tensor is
@@ -27,6 +31,16 @@ from ..gguf import quants as Q
 
 HYBRID_FAMILIES = ("qwen3next", "qwen35", "qwen35moe")
 TILED_FAMILIES = ("qwen35", "qwen35moe")
+# engine name suffix -> file name suffix, per family
+RENAMES = {"glm4moe": {"ffn_norm.weight": "post_attention_norm.weight"}}
+LAYOUT_FAMILIES = HYBRID_FAMILIES + tuple(RENAMES)
+
+
+def file_name(arch: str, name: str) -> str:
+    for a, b in RENAMES.get(arch, {}).items():
+        if name.endswith("." + a):
+            return name[: -len(a)] + b
+    return name
 
 
 def file_head(arch: str, g: int, nk: int, nv: int) -> int:
@@ -89,7 +103,7 @@ def kernel_name(arch: str, name: str) -> list[str]:
     if arch in TILED_FAMILIES and name.endswith("ssm_ba.weight"):
         base = name[: -len("ssm_ba.weight")]
         return [base + "ssm_beta.weight", base + "ssm_alpha.weight"]
-    return [name]
+    return [file_name(arch, name)]
 
 
 def to_kernel(cfg, name: str, fetch):
@@ -97,6 +111,8 @@ def to_kernel(cfg, name: str, fetch):
     returns a file tensor as (numpy uint8 bytes, qtype, shape)."""
     arch = cfg.arch
     parts = kernel_name(arch, name)
+    if arch in RENAMES:
+        return fetch(parts[0])
     if arch not in HYBRID_FAMILIES or ".ssm_" not in name and not name.endswith(
             ("attn_qkv.weight", "attn_gate.weight")):
         return fetch(name)
@@ -133,6 +149,8 @@ def to_kernel(cfg, name: str, fetch):
 
 def file_specs(cfg, specs):
     """Kernel-order tensor specs -> the family's file tensors (name, shape, qtype)."""
+    if cfg.arch in RENAMES:
+        return [(file_name(cfg.arch, n), shape, qt) for n, shape, qt in specs]
     if cfg.arch not in TILED_FAMILIES:
         return list(specs)
     out = []
@@ -151,6 +169,12 @@ def to_file(cfg, name: str, shape, qt: int, kernel_get):
     (`kernel_get(n)` -> numpy uint8 bytes): the inverse of to_kernel, at the
     float level for column moves (the random-init writer's use)."""
     arch = cfg.arch
+    if arch in RENAMES:
+        inv_names = {b: a for a, b in RENAMES[arch].items()}
+        for b, a in inv_names.items():
+            if name.endswith("." + b):
+                return kernel_get(name[: -len(b)] + a)
+        return kernel_get(name)
     if arch not in HYBRID_FAMILIES or ".ssm_" not in name and not name.endswith(
             ("attn_qkv.weight", "attn_gate.weight")):
         return kernel_get(name)

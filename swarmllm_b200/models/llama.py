@@ -170,7 +170,7 @@ class LlamaGPU:
                 L.gated = cfg.attn_output_gate
             L.experts = None
             L.post_ffn_norm = small(b + "post_ffw_norm.weight") if cfg.post_norms else None
-            if cfg.n_experts:
+            if cfg.is_moe_layer(i):
                 self._load_moe(L, b, get, small)
             else:
                 F = self.ffn_loc
@@ -280,6 +280,7 @@ class LlamaGPU:
         t, rq, _ = get(b + "ffn_gate_inp.weight")
         L.router = QLinear(t, rq, E, H, dev, f32_as_f16=True)
         L.router_b = small(b + "ffn_gate_inp.bias") if cfg.arch == "gpt-oss" else None
+        L.sel_b = small(b + "exp_probs_b.bias") if cfg.moe_gating == "sigmoid" else None
         L.sh_gu = L.sh_down = L.sh_gate = None
         if cfg.shared_expert_ffn:
             W, tr = (self.tp.world, self.tp.rank) if self.tp else (1, 0)
@@ -301,8 +302,9 @@ class LlamaGPU:
             if W > 1:
                 t = split_cols(t, qt2, shape, tr * S, (tr + 1) * S)
             L.sh_down = QLinear(t, qt2, shape[0], S, dev)
-            t, qt3, _ = get(b + "ffn_gate_inp_shexp.weight")
-            L.sh_gate = QLinear(t, qt3, 1, H, dev, f32_as_f16=True)
+            if cfg.shared_expert_gated:
+                t, qt3, _ = get(b + "ffn_gate_inp_shexp.weight")
+                L.sh_gate = QLinear(t, qt3, 1, H, dev, f32_as_f16=True)
 
     def _linears(self):
         for L in self.layers:
@@ -472,13 +474,14 @@ class LlamaGPU:
                 with P("moe"):
                     # router logits live in the side workspace only until top-k
                     moe_route(x, L.router, L.router_b, ctx.moe, ctx.gemm_side,
-                              cfg.moe_softmax_after_topk)
+                              mode=cfg.moe_mode, sel_b=L.sel_b, norm=cfg.moe_norm_topk,
+                              scale=cfg.moe_scale)
                     sh = shg = None
                     if L.sh_gu is not None:
                         S = L.sh_gu.rows // 2
                         g = L.sh_gu(x, ctx.gemm)
                         C().epi_swiglu(g, None, S, 0, False, 0.0, 0.0, ctx.act_sh[:N])
-                        shg = L.sh_gate(x, ctx.gemm_side)
+                        shg = L.sh_gate(x, ctx.gemm_side) if L.sh_gate is not None else None
                         sh = L.sh_down(ctx.act_sh[:N], ctx.gemm)
                     if self.tp is not None:
                         g = moe_experts_tp(x, L.experts, ctx.moe, self.tp, sh, shg)
@@ -581,8 +584,9 @@ class GpuForwardContext:
             self.lora_delta = torch.zeros(max_tokens * rows, dtype=torch.float32, device=dev)
             self.lora_u = torch.zeros(max_tokens * R, dtype=torch.float32, device=dev)
         self.moe = None
-        if cfg.n_experts:
-            ex = next(L.experts for L in model.layers if L.experts is not None)
+        exs = [L.experts for L in model.layers if L.experts is not None]
+        if exs:
+            ex = exs[0]
             self.moe = MoeWorkspace(dev, max_tokens, H, cfg.expert_ffn, cfg.n_experts,
                                     cfg.n_experts_used, ex.x_dtype, self.gemm.num_sms,
                                     ep=model.ep)
@@ -723,7 +727,7 @@ class LlamaCPU:
     def _load_ffn_cpu(self, L, b, dq, lw=None):
         cfg = self.cfg
         lw = lw or dq
-        L.moe = bool(cfg.n_experts)
+        L.moe = cfg.is_moe_layer(int(b.split(".")[1]))
         if L.moe:
             gpt = cfg.arch == "gpt-oss"
             L.wr = dq(b + "ffn_gate_inp.weight")
@@ -733,11 +737,13 @@ class LlamaCPU:
             L.ebg = dq(b + "ffn_gate_exps.bias") if gpt else None
             L.ebu = dq(b + "ffn_up_exps.bias") if gpt else None
             L.ebd = dq(b + "ffn_down_exps.bias") if gpt else None
-            L.sg = None
+            L.sel_b = dq(b + "exp_probs_b.bias") if cfg.moe_gating == "sigmoid" else None
+            L.sg = L.sgi = None
             if cfg.shared_expert_ffn:
                 L.sg, L.su, L.sd = (dq(b + n) for n in ("ffn_gate_shexp.weight", "ffn_up_shexp.weight",
                                                          "ffn_down_shexp.weight"))
-                L.sgi = dq(b + "ffn_gate_inp_shexp.weight")
+                if cfg.shared_expert_gated:
+                    L.sgi = dq(b + "ffn_gate_inp_shexp.weight")
         elif cfg.fused_gate_up:
             gu = lw(b + "ffn_up.weight")
             L.wg, L.wu, L.wd = gu[:cfg.ffn], gu[cfg.ffn:], lw(b + "ffn_down.weight")
@@ -870,11 +876,21 @@ class LlamaCPU:
         cfg = self.cfg
         k = cfg.n_experts_used
         logits = x @ L.wr.T + (L.br if L.br is not None else 0)
-        top_v, top_i = torch.topk(logits, k, dim=-1)
-        if cfg.moe_softmax_after_topk:
-            w = torch.softmax(top_v, -1)
+        if cfg.moe_gating == "sigmoid":
+            # sigmoid scores; the selection bias picks the experts but does not weigh them
+            score = torch.sigmoid(logits)
+            sel = score + (L.sel_b if L.sel_b is not None else 0)
+            top_i = torch.topk(sel, k, dim=-1).indices
+            w = torch.gather(score, 1, top_i)
+            if cfg.moe_norm_topk:
+                w = w / w.sum(-1, keepdim=True)
+            w = w * cfg.moe_scale
         else:
-            w = torch.gather(torch.softmax(logits, -1), 1, top_i)
+            top_v, top_i = torch.topk(logits, k, dim=-1)
+            if cfg.moe_softmax_after_topk:
+                w = torch.softmax(top_v, -1)
+            else:
+                w = torch.gather(torch.softmax(logits, -1), 1, top_i)
         y = torch.zeros_like(x)
         for e in top_i.unique().tolist():
             sel = top_i == e
@@ -886,7 +902,7 @@ class LlamaCPU:
             o = self._act(g, u) @ L.ed[e].T + (L.ebd[e] if L.ebd is not None else 0)
             y[rows] += we[:, None] * o
         if L.sg is not None:
-            gate = torch.sigmoid(x @ L.sgi)[:, None]
+            gate = torch.sigmoid(x @ L.sgi)[:, None] if L.sgi is not None else 1.0
             y = y + gate * ((torch.nn.functional.silu(x @ L.sg.T) * (x @ L.su.T)) @ L.sd.T)
         return y
 

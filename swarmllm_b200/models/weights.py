@@ -21,7 +21,7 @@ import torch
 from ..gguf import quants as Q
 from ..gguf.file import GGUFReader, GGUFWriter, ShardedGguf
 from .config import ModelConfig, from_gguf_metadata, to_gguf_metadata
-from .layout import HYBRID_FAMILIES, file_specs, kernel_name, to_file, to_kernel
+from .layout import LAYOUT_FAMILIES, file_specs, kernel_name, to_file, to_kernel
 
 
 def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
@@ -71,7 +71,7 @@ def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
             if cfg.attn_sinks:
                 specs.append((b + "attn_sinks.weight", (cfg.n_heads,), Q.F32))
         specs.append((b + "ffn_norm.weight", (H,), Q.F32))
-        if cfg.n_experts:
+        if cfg.is_moe_layer(i):
             E, F = cfg.n_experts, cfg.expert_ffn
             specs += [(b + "ffn_gate_inp.weight", (E, H), Q.F32),
                       (b + "ffn_gate_exps.weight", (E, F, H), xq),
@@ -82,12 +82,15 @@ def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
                           (b + "ffn_gate_exps.bias", (E, F), Q.F32),
                           (b + "ffn_up_exps.bias", (E, F), Q.F32),
                           (b + "ffn_down_exps.bias", (E, H), Q.F32)]
+            if cfg.moe_gating == "sigmoid":
+                specs.append((b + "exp_probs_b.bias", (E,), Q.F32))
             if cfg.shared_expert_ffn:
                 S = cfg.shared_expert_ffn
                 specs += [(b + "ffn_gate_shexp.weight", (S, H), wq),
                           (b + "ffn_up_shexp.weight", (S, H), wq),
-                          (b + "ffn_down_shexp.weight", (H, S), wq),
-                          (b + "ffn_gate_inp_shexp.weight", (H,), Q.F32)]
+                          (b + "ffn_down_shexp.weight", (H, S), wq)]
+                if cfg.shared_expert_gated:
+                    specs.append((b + "ffn_gate_inp_shexp.weight", (H,), Q.F32))
         elif cfg.fused_gate_up:
             specs += [(b + "ffn_up.weight", (2 * cfg.ffn, H), wq),
                       (b + "ffn_down.weight", (H, cfg.ffn), wq)]
@@ -126,6 +129,8 @@ def _init_value(name: str, shape, rng: np.random.Generator, std: float) -> np.nd
         return rng.uniform(-1, 1, shape).astype(np.float32)
     if name.endswith("attn_sinks.weight"):
         return rng.standard_normal(shape).astype(np.float32)
+    if name.endswith("exp_probs_b.bias"):
+        return rng.uniform(-0.05, 0.05, shape).astype(np.float32)
     if name.endswith("ffn_gate_inp.weight"):
         # routers: peaked top-k (logit std ~ 5) like trained routers, not near-uniform
         return (rng.standard_normal(shape, dtype=np.float32) * (5.0 / np.sqrt(shape[-1]))).astype(np.float32)
@@ -140,6 +145,9 @@ class GgufSource:
         else:
             self.f = GGUFReader(path)
         self.cfg = from_gguf_metadata(self.f.metadata)
+        if self.cfg.arch == "glm4moe" and "swarmllm.config" not in self.f.metadata:
+            # GLM-4.5 files say whether they carry q/k norms by the tensors alone
+            self.cfg.qk_norm = "blk.0.attn_q_norm.weight" in self.f.tensors
         # LongRoPE (phi3): per-pair frequency divisors stored as tensors; the
         # short factors serve contexts up to the original training length
         for name in ("rope_factors_short.weight", "rope_factors_long.weight"):
@@ -157,7 +165,7 @@ class GgufSource:
     def get(self, name: str, device=None):
         """A tensor as (bytes, qtype, shape), in the kernels' order: the hybrid
         families' DeltaNet tensors are reordered from the file's (layout.py)."""
-        if self.cfg.arch in HYBRID_FAMILIES:
+        if self.cfg.arch in LAYOUT_FAMILIES:
             raw, qt, shape = to_kernel(self.cfg, name, self._raw)
         else:
             raw, qt, shape = self._raw(name)

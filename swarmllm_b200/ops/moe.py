@@ -130,11 +130,17 @@ class MoeWorkspace:
 
 
 def moe_route(x: torch.Tensor, router, router_b: torch.Tensor | None, ws: MoeWorkspace,
-              gemm, softmax_after_topk: bool = True):
-    """Router logits (QLinear on `gemm`) -> top-k ids / weights / counts in ws."""
+              gemm, softmax_after_topk: bool = True, mode: int | None = None,
+              sel_b: torch.Tensor | None = None, norm: bool = True, scale: float = 1.0):
+    """Router logits (QLinear on `gemm`) -> top-k ids / weights / counts in ws.
+    mode: 0 softmax over all experts, 1 top-k then softmax (the default from
+    `softmax_after_topk`), 2 sigmoid scores chosen with the selection bias
+    `sel_b`, renormalised over the k when `norm`, times `scale`."""
     T = x.shape[0]
     lg = router(x, gemm)
-    C().moe_topk(lg, router_b, T, ws.E, ws.k, softmax_after_topk, ws.ids, ws.wts, ws.counts)
+    m = mode if mode is not None else (1 if softmax_after_topk else 0)
+    C().moe_topk(lg, router_b, T, ws.E, ws.k, m, sel_b, norm, float(scale), ws.ids, ws.wts,
+                 ws.counts)
 
 
 def moe_experts(x: torch.Tensor, experts: MoeExperts, ws: MoeWorkspace, residual: torch.Tensor,
@@ -212,7 +218,8 @@ def moe_experts_tp(x: torch.Tensor, experts: MoeExperts, ws: MoeWorkspace, tp, s
 
 
 def moe_ffn(x, experts, router, router_b, ws, gemm, residual, norm_w, out, eps,
-            softmax_after_topk: bool = True, shared=None, shared_gate=None):
-    """Routing + experts + combine in one call (no shared expert between)."""
-    moe_route(x, router, router_b, ws, gemm, softmax_after_topk)
+            softmax_after_topk: bool = True, shared=None, shared_gate=None, **route):
+    """Routing + experts + combine in one call (no shared expert between);
+    `route`: moe_route's mode / sel_b / norm / scale."""
+    moe_route(x, router, router_b, ws, gemm, softmax_after_topk, **route)
     moe_experts(x, experts, ws, residual, norm_w, out, eps, shared, shared_gate)

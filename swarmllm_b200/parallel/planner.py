@@ -50,7 +50,7 @@ def layer_weight_bytes(cfg: ModelConfig, layer: int) -> tuple[float, float]:
     else:
         q = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
         mix = _qbytes(wq, H * (q + 2 * cfg.kv_dim)) + _qbytes(wq, cfg.q_dim * H)
-    if cfg.n_experts:
+    if cfg.is_moe_layer(layer):
         xq = cfg.expert_qtype or wq
         per_expert = 3 * _qbytes(xq, H * cfg.expert_ffn)
         shared = 3 * _qbytes(wq, H * cfg.shared_expert_ffn) if cfg.shared_expert_ffn else 0.0
@@ -66,7 +66,7 @@ def layer_costs(cfg: ModelConfig, batch: int, context: int, tp: int = 1,
     out = []
     for l in range(cfg.n_layers):
         read, _ = layer_weight_bytes(cfg, l)
-        if cfg.n_experts:  # the experts this batch routes to (uniform routing)
+        if cfg.is_moe_layer(l):  # the experts this batch routes to (uniform routing)
             used = cfg.n_experts * (1 - (1 - cfg.n_experts_used / cfg.n_experts) ** batch)
             xq = cfg.expert_qtype or cfg.weight_qtype
             read += used * 3 * _qbytes(xq, cfg.hidden * cfg.expert_ffn)

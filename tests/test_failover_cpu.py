@@ -75,9 +75,11 @@ def _worker(rank, world, port, ctl_port, crash_rank, crash_after, q, waves=False
         return eng
 
     # grace well above the group timeout: a survivor that learns of the failure
-    # only from its own 5 s timeout must still register on a loaded machine
-    rp = ResilientPipeline(build, rank, world, "127.0.0.1", ctl_port, pg_timeout_s=5.0,
-                           grace_s=15.0)
+    # only from its own group timeout must still register on a loaded machine;
+    # the timeout itself stays above a step's time when the host is busy (a
+    # healthy step that overruns it would be taken for a second failure)
+    rp = ResilientPipeline(build, rank, world, "127.0.0.1", ctl_port, pg_timeout_s=10.0,
+                           grace_s=25.0)
     out = rp.generate(_prompts(), SamplingParams(max_tokens=10, ignore_eos=True))
     if rank == 0:
         q.put((out, rp.recoveries, rp.members))

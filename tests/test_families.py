@@ -15,9 +15,11 @@ def family_cfg(fam: str):
               output_qtype="Q8_0", rope_theta=10000.0, sliding_window=24)
     if fam == "phi3":
         kw.update(hidden=768, n_heads=8, n_kv_heads=8, head_dim=96, ffn=1536)
-    if fam in ("qwen2moe", "qwen3moe"):
+    if fam in ("qwen2moe", "qwen3moe", "glm4moe"):
         kw.update(n_experts=8, n_experts_used=2, expert_ffn=256, weight_qtype="Q4_K",
-                  output_qtype="Q4_K", shared_expert_ffn=256 if fam == "qwen2moe" else 0)
+                  output_qtype="Q4_K", shared_expert_ffn=256 if fam != "qwen3moe" else 0)
+    if fam == "glm4moe":
+        kw.update(moe_dense_layers=1, moe_scale=1.5, qk_norm=True)
     cfg = apply_family(ModelConfig(**kw))
     if fam == "gemma3":
         cfg.rope_theta = 1e6
@@ -25,7 +27,7 @@ def family_cfg(fam: str):
 
 
 FAMILIES = ["mistral", "qwen2", "qwen3", "qwen2moe", "qwen3moe", "gemma", "gemma2", "gemma3",
-            "phi3", "glm4"]
+            "phi3", "glm4", "glm4moe"]
 
 
 def test_family_options():
@@ -79,3 +81,66 @@ def test_family_gguf_roundtrip_and_cpu_forward(fam, tmp_path):
         outs.append(m.forward(b, kv))
     assert torch.isfinite(outs[0]).all()
     assert torch.allclose(outs[0], outs[1])
+
+
+def test_glm4moe_file_layout_and_metadata(tmp_path):
+    """GLM-4.5 files: the FFN pre-norm is named post_attention_norm, the first
+    layers are dense, routed layers carry the selection bias and an ungated
+    shared expert; the file's own keys (no engine blob) give the routing."""
+    from swarmllm_b200.gguf.file import GGUFReader
+    from swarmllm_b200.models.config import from_gguf_metadata, to_gguf_metadata
+    from swarmllm_b200.models.weights import GgufSource, RandomSource, write_random_gguf
+    cfg = family_cfg("glm4moe")
+    path = write_random_gguf(cfg, str(tmp_path / "g.gguf"), seed=1)
+    names = set(GGUFReader(path).tensors)
+    assert "blk.0.post_attention_norm.weight" in names and "blk.0.ffn_norm.weight" not in names
+    assert "blk.0.ffn_gate.weight" in names and "blk.0.ffn_gate_exps.weight" not in names
+    assert "blk.1.ffn_gate_exps.weight" in names and "blk.1.exp_probs_b.bias" in names
+    assert "blk.1.ffn_gate_inp_shexp.weight" not in names
+    src = GgufSource(path)
+    a, _, _ = src.get("blk.1.ffn_norm.weight")
+    b, _, _ = RandomSource(cfg, seed=1).get("blk.1.ffn_norm.weight")
+    assert torch.equal(a, b)
+    md = to_gguf_metadata(cfg)
+    md.pop("swarmllm.config")
+    md["general.architecture"] = "glm4moe"
+    md["glm4moe.block_count"] = cfg.n_layers + 1
+    md["glm4moe.nextn_predict_layers"] = 1
+    c = from_gguf_metadata(md)
+    assert c.n_layers == cfg.n_layers and c.moe_gating == "sigmoid" and c.moe_mode == 2
+    assert c.moe_dense_layers == 1 and c.moe_scale == 1.5 and c.moe_norm_topk
+    assert c.shared_expert_ffn == cfg.expert_ffn and not c.shared_expert_gated
+    assert [c.is_moe_layer(i) for i in range(3)] == [False, True, True]
+
+
+def test_sigmoid_routing_oracle():
+    """Sigmoid gating: the selection bias decides which experts run, the
+    weights are the unbiased scores (renormalised, scaled)."""
+    from swarmllm_b200.models.llama import LlamaCPU, _GpuLayer
+    cfg = family_cfg("glm4moe")
+    m = LlamaCPU.__new__(LlamaCPU)
+    m.cfg = cfg
+    L = _GpuLayer()
+    E, H, F = cfg.n_experts, cfg.hidden, cfg.expert_ffn
+    g = torch.Generator().manual_seed(0)
+    L.wr = torch.randn(E, H, generator=g) * 0.05
+    L.br = None
+    L.sel_b = torch.zeros(E)
+    L.sel_b[5] = 10.0                               # expert 5 always selected
+    L.eg = torch.randn(E, F, H, generator=g) * 0.02
+    L.eu = torch.randn(E, F, H, generator=g) * 0.02
+    L.ed = torch.randn(E, H, F, generator=g) * 0.02
+    L.ebg = L.ebu = L.ebd = None
+    L.sg = L.sgi = None
+    x = torch.randn(3, H, generator=g)
+    y = m._moe(x, L)
+    score = torch.sigmoid(x @ L.wr.T)
+    want = torch.zeros_like(x)
+    for t in range(3):
+        sel = torch.topk(score[t] + L.sel_b, 2).indices
+        assert 5 in sel.tolist()
+        w = score[t, sel] / score[t, sel].sum() * cfg.moe_scale
+        for e, we in zip(sel.tolist(), w):
+            a = torch.nn.functional.silu(x[t] @ L.eg[e].T) * (x[t] @ L.eu[e].T)
+            want[t] += we * (a @ L.ed[e].T)
+    assert torch.allclose(y, want, atol=1e-5)
