@@ -169,6 +169,7 @@ class LlamaGPU:
                 L.window = cfg.sliding_window if cfg.is_swa(i) else 0
                 L.gated = cfg.attn_output_gate
             L.experts = None
+            L.sh_gu = L.sh_down = L.sh_gate = L.sel_b = None
             L.post_ffn_norm = small(b + "post_ffw_norm.weight") if cfg.post_norms else None
             if cfg.is_moe_layer(i):
                 self._load_moe(L, b, get, small)
@@ -401,7 +402,7 @@ class LlamaGPU:
                 # expert parallelism send-counts/dispatch/wait/plan/2 GEMMs/wait/combine
                 # (tensor parallelism: localize/plan/scatter/2 GEMMs/partial store/reduce)
                 n += 2 + (8 if self.ep is not None else 7 if self.tp is not None else 5) + \
-                    (4 if L.sh_gu is not None else 0)
+                    (3 + (L.sh_gate is not None) if L.sh_gu is not None else 0)
             else:
                 n += 4   # gate|up GEMM, SwiGLU, down GEMM, residual+norm
         if self.last:
