@@ -201,3 +201,49 @@ int cpu_paged_attention(const AttnArgs& a, const void* k_cache, const void* v_ca
 }
 
 }  // namespace swarm_native
+
+namespace swarm_native {
+
+void cpu_delta_rule(const float* q, const float* k, const float* v, const float* g,
+                    const float* beta, float* state, float* out, int T, int nk, int nv, int dk,
+                    int dv) {
+  const int rep = nv / nk;
+#pragma omp parallel for schedule(static)
+  for (int h = 0; h < nv; ++h) {
+    float* S = state + (size_t)h * dk * dv;
+    std::vector<float> kv(dv), d(dv);
+    const int kh = h / rep;
+    for (int t = 0; t < T; ++t) {
+      const float* kt = k + ((size_t)t * nk + kh) * dk;
+      const float* qt = q + ((size_t)t * nk + kh) * dk;
+      const float* vt = v + ((size_t)t * nv + h) * dv;
+      const float decay = std::exp(g[(size_t)t * nv + h]);
+      const float b = beta[(size_t)t * nv + h];
+      std::fill(kv.begin(), kv.end(), 0.f);
+      for (int i = 0; i < dk; ++i) {  // decay the state and read it at k in one pass
+        float* Si = S + (size_t)i * dv;
+        const float ki = kt[i];
+#pragma omp simd
+        for (int j = 0; j < dv; ++j) {
+          Si[j] *= decay;
+          kv[j] += Si[j] * ki;
+        }
+      }
+#pragma omp simd
+      for (int j = 0; j < dv; ++j) d[j] = b * (vt[j] - kv[j]);
+      float* o = out + ((size_t)t * nv + h) * dv;
+      std::fill(o, o + dv, 0.f);
+      for (int i = 0; i < dk; ++i) {  // rank-1 update, then read at q
+        float* Si = S + (size_t)i * dv;
+        const float ki = kt[i], qi = qt[i];
+#pragma omp simd
+        for (int j = 0; j < dv; ++j) {
+          Si[j] += ki * d[j];
+          o[j] += Si[j] * qi;
+        }
+      }
+    }
+  }
+}
+
+}  // namespace swarm_native

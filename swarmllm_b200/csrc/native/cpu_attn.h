@@ -29,3 +29,16 @@ void cpu_silu_mul(const float* g, const float* u, float* out, int64_t n, float l
 float exp_approx(float x);
 
 }  // namespace swarm_native
+
+namespace swarm_native {
+
+// Gated delta rule over one sequence's rows, per value head h (OpenMP over
+// heads), state S [nv][dk][dv] fp32 updated in place:
+//   S = exp(g[t,h]) S;  d = beta[t,h] (v_t - S^T k_t);  S += k_t d^T;  o_t = S^T q_t
+// q, k [T][nk][dk] (value head h reads key head h / (nv / nk)), v, out
+// [T][nv][dv], g, beta [T][nv].
+void cpu_delta_rule(const float* q, const float* k, const float* v, const float* g,
+                    const float* beta, float* state, float* out, int T, int nk, int nv, int dk,
+                    int dv);
+
+}  // namespace swarm_native

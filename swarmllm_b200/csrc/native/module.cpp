@@ -184,6 +184,33 @@ PYBIND11_MODULE(_native, m) {
         return out;
       },
       py::arg("g"), py::arg("u"), py::arg("limit") = 0.f, py::arg("alpha") = 1.702f);
+  m.def(
+      "cpu_delta_rule",
+      [](f32a q, f32a k, f32a v, f32a g, f32a beta,
+         py::array_t<float, py::array::c_style> state) {
+        if (q.ndim() != 3 || k.ndim() != 3 || v.ndim() != 3 || state.ndim() != 3)
+          throw std::invalid_argument("q, k [T, nk, dk], v [T, nv, dv], state [nv, dk, dv]");
+        const int T = (int)q.shape(0), nk = (int)q.shape(1), dk = (int)q.shape(2);
+        const int nv = (int)v.shape(1), dv = (int)v.shape(2);
+        if (k.shape(0) != T || k.shape(1) != nk || k.shape(2) != dk || v.shape(0) != T ||
+            g.size() != (py::ssize_t)T * nv || beta.size() != (py::ssize_t)T * nv ||
+            state.shape(0) != nv || state.shape(1) != dk || state.shape(2) != dv ||
+            nk <= 0 || nv % nk != 0)
+          throw std::invalid_argument("delta rule shapes");
+        if (!state.writeable()) throw std::invalid_argument("state must be writeable");
+        py::array_t<float> out({(py::ssize_t)T, (py::ssize_t)nv, (py::ssize_t)dv});
+        const float *qp = q.data(), *kp = k.data(), *vp = v.data(), *gp = g.data(),
+                    *bp = beta.data();
+        float* sp = state.mutable_data();
+        float* op = out.mutable_data();
+        {
+          py::gil_scoped_release nogil;
+          cpu_delta_rule(qp, kp, vp, gp, bp, sp, op, T, nk, nv, dk, dv);
+        }
+        return out;
+      },
+      py::arg("q"), py::arg("k"), py::arg("v"), py::arg("g"), py::arg("beta"), py::arg("state"),
+      "gated delta rule over T rows; state [nv, dk, dv] fp32 updated in place");
   m.def("exp_approx", [](f32a x) {
     py::array_t<float> out(std::vector<py::ssize_t>(x.shape(), x.shape() + x.ndim()));
     for (py::ssize_t i = 0; i < x.size(); ++i) out.mutable_data()[i] = exp_approx(x.data()[i]);

@@ -849,6 +849,10 @@ class LlamaCPU:
             act = torch.nn.functional.silu(act)
             conv_st[slot] = xs[-(K - 1):].to(conv_st.dtype)
             S = torch.zeros(nv, D, D, dtype=x.dtype) if p0 == 0 else ssm_st[slot].to(x.dtype)
+            if self.native:
+                out[r0:r0 + n] = self._deltanet_native(L, act, ba[r0:r0 + n], z[r0:r0 + n], S)
+                ssm_st[slot] = S.to(ssm_st.dtype)
+                continue
             for t in range(n):
                 a = act[t]
                 q = a[:nk * D].view(nk, D)
@@ -870,6 +874,29 @@ class LlamaCPU:
                 out[r] = o.flatten()
             ssm_st[slot] = S.to(ssm_st.dtype)
         return out @ L.w_out.T
+
+    def _deltanet_native(self, L, act, ba, z, S):
+        """The same recurrence with the per-row gates and norms as whole-block
+        torch ops and the state update in the native kernel (S in place)."""
+        from .. import _native
+        cfg = self.cfg
+        nk, nv, D = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
+        n = act.shape[0]
+        q = act[:, :nk * D].reshape(n, nk, D)
+        k = act[:, nk * D:2 * nk * D].reshape(n, nk, D)
+        v = act[:, 2 * nk * D:].reshape(n, nv, D)
+        q = q * torch.rsqrt(q.pow(2).sum(-1, keepdim=True) + 1e-6) / math.sqrt(D)
+        k = k * torch.rsqrt(k.pow(2).sum(-1, keepdim=True) + 1e-6)
+        beta = torch.sigmoid(ba[:, :nv])
+        g = L.A * torch.nn.functional.softplus(ba[:, nv:] + L.dt_bias)
+        st = S.numpy()
+        o = torch.from_numpy(_native.cpu_delta_rule(
+            q.float().contiguous().numpy(), k.float().contiguous().numpy(),
+            v.float().contiguous().numpy(), g.float().contiguous().numpy(),
+            beta.float().contiguous().numpy(), st))
+        o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + cfg.rms_eps) * L.ssm_norm
+        o = o * torch.nn.functional.silu(z.reshape(n, nv, D))
+        return o.reshape(n, nv * D)
 
     def _moe(self, x, L):
         """Routed experts (top-k softmax) + optional sigmoid-gated shared expert

@@ -45,3 +45,55 @@ def test_native_cpu_path_matches_oracle(fam, qtype):
         assert rel < 3e-2, rel
         cos = torch.nn.functional.cosine_similarity(n.flatten(), r.flatten(), dim=0)
         assert cos > 0.999
+
+
+def test_native_delta_rule_matches_recurrence():
+    from swarmllm_b200 import _native
+    g_ = torch.Generator().manual_seed(0)
+    T, nk, nv, D = 7, 2, 4, 32
+    q = torch.nn.functional.normalize(torch.randn(T, nk, D, generator=g_), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(T, nk, D, generator=g_), dim=-1)
+    v = torch.randn(T, nv, D, generator=g_)
+    g = -torch.rand(T, nv, generator=g_)
+    beta = torch.rand(T, nv, generator=g_)
+    S0 = torch.randn(nv, D, D, generator=g_) * 0.1
+    S = S0.clone()
+    out = torch.from_numpy(_native.cpu_delta_rule(q.numpy(), k.numpy(), v.numpy(), g.numpy(),
+                                                  beta.numpy(), S.numpy()))
+    R = S0.clone()
+    qq, kk = q.repeat_interleave(nv // nk, 1), k.repeat_interleave(nv // nk, 1)
+    for t in range(T):
+        R = R * torch.exp(g[t])[:, None, None]
+        kv = torch.einsum("hij,hi->hj", R, kk[t])
+        R = R + kk[t][:, :, None] * ((v[t] - kv) * beta[t][:, None])[:, None, :]
+        assert torch.allclose(out[t], torch.einsum("hij,hi->hj", R, qq[t]), atol=1e-5)
+    assert torch.allclose(S, R, atol=1e-5)
+
+
+def test_native_hybrid_model_matches_oracle():
+    from test_hybrid_cpu import tiny_hybrid
+    from swarmllm_b200.models.llama import LlamaCPU, StepBatch
+    from swarmllm_b200.models.weights import RandomSource
+    from swarmllm_b200.ops.attention import PagedKVCache
+    cfg = tiny_hybrid()
+    src = RandomSource(cfg, seed=2)
+    T = 20
+    toks = torch.from_numpy(np.random.default_rng(0).integers(0, cfg.vocab, T).astype(np.int32))
+    pos = torch.arange(T, dtype=torch.int32)
+    bt = torch.arange(4, dtype=torch.int32).repeat(T, 1)
+    outs = []
+    for native in (False, True):
+        m = LlamaCPU(cfg, src, native=native)
+        kv = PagedKVCache(m.n_kv_layers, 4, cfg.n_kv_heads, cfg.head_dim, "cpu")
+        spec = m.linear_state_spec()
+        kv.add_linear_state(spec[0], 1, *spec[1:])
+        res = []
+        for lo, hi in ((0, 12), (12, T)):          # two chunks: the state carries over
+            sl = slice(lo, hi)
+            b = StepBatch(toks[sl], pos[sl], pos[sl], bt[sl], pos[sl] + 1,
+                          torch.arange(hi - lo), 64,
+                          ssm_seqs=torch.tensor([[0, hi - lo, 0, lo]], dtype=torch.int32))
+            res.append(m.forward(b, kv))
+        outs.append(torch.cat(res))
+    rel = (outs[1] - outs[0]).norm() / outs[0].norm()
+    assert rel < 3e-2, rel
