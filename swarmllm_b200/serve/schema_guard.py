@@ -8,9 +8,11 @@ array items and item counts (`items`, `minItems`, `maxItems`), `enum` /
 `const` values, integers versus numbers, string `pattern`s (regex_guard.py:
 the ECMA subset without back-references or look-around), the fixed-shape
 `format`s (date, time, date-time, uuid, ipv4, email), `minLength` /
-`maxLength`, and `anyOf` / `oneOf` alternatives.  It is a set of
-deterministic parsers, one per alternative still open: a character is
-accepted if at least one parser takes it.  Numeric ranges are not enforced.  A parser
+`maxLength`, numeric ranges (`minimum` / `maximum` and their exclusive forms;
+a bounded number is written without an exponent, and a prefix is live only
+while some completion of it lies in the range), and `anyOf` / `oneOf`
+alternatives.  It is a set of deterministic parsers, one per alternative
+still open: a character is accepted if at least one parser takes it.  A parser
 never takes a character after which the value could not be completed (a ','
 with no unseen allowed key left, a '}' with a required key missing, a ']' short
 of minItems), so decoding cannot paint itself into a corner.  Whitespace
@@ -24,6 +26,7 @@ schema (src/inference/reply_grammar.rs:90,156).
 from __future__ import annotations
 
 import json
+from decimal import Decimal
 
 from .regex_guard import FORMAT_PATTERNS, compile_pattern
 
@@ -141,7 +144,7 @@ class _Parser:
     """One deterministic parse under one choice of anyOf / oneOf alternatives."""
 
     __slots__ = ("stack", "exp", "tok", "key", "uni", "num", "integer", "lit", "lpos",
-                 "cands", "text", "pending", "ws", "nl", "scon", "sst", "slen", "uhex")
+                 "cands", "text", "pending", "ws", "nl", "scon", "sst", "slen", "uhex", "nrule", "ntext")
 
     def __init__(self):
         self.stack: list = []
@@ -161,12 +164,14 @@ class _Parser:
         self.sst = None                # its patterns' NFA state sets
         self.slen = 0                  # characters of the string so far
         self.uhex = ""                 # hex digits of a \u escape
+        self.nrule = None              # _NumRule of the number being read, if any
+        self.ntext = ""                # ... its text so far
 
     def copy(self) -> "_Parser":
         c = _Parser.__new__(_Parser)
         c.stack = [f.copy() for f in self.stack]
         for f in ("exp", "tok", "key", "uni", "num", "integer", "lit", "lpos", "text",
-                  "pending", "ws", "nl", "scon", "sst", "slen", "uhex"):
+                  "pending", "ws", "nl", "scon", "sst", "slen", "uhex", "nrule", "ntext"):
             setattr(c, f, getattr(self, f))
         c.cands = list(self.cands)
         return c
@@ -221,8 +226,12 @@ class _Parser:
             self.sst = self.scon.start() if self.scon is not None else None
             return True
         if (c == "-" or c in _DIGITS) and (ok("number") or ok("integer")):
-            self.tok = _NUM
             self.integer = types is not None and "number" not in types
+            self.nrule = _NumRule.of(schema, self.integer)
+            if self.nrule is not None and not self.nrule.viable(c):
+                return False
+            self.tok = _NUM
+            self.ntext = c
             self.num = _N_SIGN if c == "-" else (_N_ZERO if c == "0" else _N_INT)
             return True
         for lit, t in (("true", "boolean"), ("false", "boolean"), ("null", "null")):
@@ -277,7 +286,11 @@ class _Parser:
             return True
         if t == _NUM:
             n = self.num
+            if self.nrule is not None and (c in _DIGITS or c == "."):
+                if not self.nrule.viable(self.ntext + c):
+                    return False
             if c in _DIGITS:
+                self.ntext += c
                 if n == _N_SIGN:
                     self.num = _N_ZERO if c == "0" else _N_INT
                 elif n == _N_ZERO:
@@ -290,8 +303,9 @@ class _Parser:
             if not self.integer:
                 if c == "." and n in (_N_ZERO, _N_INT):
                     self.num = _N_DOT
+                    self.ntext += c
                     return True
-                if c in "eE" and n in (_N_ZERO, _N_INT, _N_FRAC):
+                if c in "eE" and n in (_N_ZERO, _N_INT, _N_FRAC) and self.nrule is None:
                     self.num = _N_E
                     return True
                 if c in "+-" and n == _N_E:
@@ -299,7 +313,10 @@ class _Parser:
                     return True
             if n not in _NUM_END_OK:
                 return False
+            if self.nrule is not None and not self.nrule.contains(Decimal(self.ntext)):
+                return False
             self.tok = _NONE
+            self.nrule = None
             self._end_value()
             if not self.stack:
                 return c in _WS
@@ -455,6 +472,109 @@ class _StrRule:
 
     def complete(self, states, n: int) -> bool:
         return n >= self.min_len and all(p.accepts(st) for p, st in zip(self.pats, states))
+
+
+_NUM_PREFIX = __import__("re").compile(r"-?(\d+(\.\d*)?)?$")
+
+
+def _dec(v):
+    return Decimal(str(v)) if isinstance(v, (int, float)) and not isinstance(v, bool) else None
+
+
+class _NumRule:
+    """`minimum` / `maximum` (inclusive) and `exclusiveMinimum` /
+    `exclusiveMaximum` (numbers, or draft-4 booleans) of one number."""
+
+    __slots__ = ("lo", "lo_ex", "hi", "hi_ex", "integer")
+
+    @staticmethod
+    def of(schema: dict, integer: bool) -> "_NumRule | None":
+        lo, hi = _dec(schema.get("minimum")), _dec(schema.get("maximum"))
+        lo_ex = hi_ex = False
+        xmin, xmax = schema.get("exclusiveMinimum"), schema.get("exclusiveMaximum")
+        if xmin is True:
+            lo_ex = lo is not None
+        elif _dec(xmin) is not None and (lo is None or _dec(xmin) >= lo):
+            lo, lo_ex = _dec(xmin), True
+        if xmax is True:
+            hi_ex = hi is not None
+        elif _dec(xmax) is not None and (hi is None or _dec(xmax) <= hi):
+            hi, hi_ex = _dec(xmax), True
+        if lo is None and hi is None:
+            return None
+        r = _NumRule()
+        r.lo, r.lo_ex, r.hi, r.hi_ex, r.integer = lo, lo_ex, hi, hi_ex, integer
+        return r
+
+    def contains(self, x: Decimal) -> bool:
+        if self.lo is not None and (x < self.lo or (self.lo_ex and x == self.lo)):
+            return False
+        if self.hi is not None and (x > self.hi or (self.hi_ex and x == self.hi)):
+            return False
+        return True
+
+    def _meets(self, a: Decimal, a_in: bool, b: Decimal | None, b_in: bool) -> bool:
+        """Does the value interval from a to b (None: unbounded above) meet
+        the allowed range?  a_in / b_in: whether the ends belong to it."""
+        lo, lo_in = (a, a_in)
+        if self.lo is not None and (self.lo > lo or (self.lo == lo and self.lo_ex)):
+            lo, lo_in = self.lo, not self.lo_ex
+        hi, hi_in = (b, b_in)
+        if self.hi is not None and (hi is None or self.hi < hi or (self.hi == hi and self.hi_ex)):
+            hi, hi_in = self.hi, not self.hi_ex
+        if hi is None:
+            return True
+        return lo < hi or (lo == hi and lo_in and hi_in)
+
+    def viable(self, text: str) -> bool:
+        """Some completion of the number prefix `text` (sign, digits, an
+        optional '.' and fraction digits) lies in the range."""
+        if not _NUM_PREFIX.match(text):
+            return True                    # not number syntax: the parser refuses it
+        neg = text.startswith("-")
+        body = text[1:] if neg else text
+        if body == "":                     # just the sign: any magnitude
+            return self._side(neg, [(Decimal(0), True, None, False)])
+        ip, dot, fp = body.partition(".")
+        if dot:
+            a = Decimal(ip + "." + (fp or "0"))
+            step = Decimal(1).scaleb(-len(fp)) if fp else Decimal(1)
+            return self._side(neg, [(a, True, a + step, False)])
+        I = Decimal(ip)
+        if I == 0:                         # "0" or "0.xxx"
+            return self._side(neg, [(Decimal(0), True, Decimal(0) if self.integer else Decimal(1),
+                                     self.integer)])
+        ivs = []
+        bound = max(abs(v) for v in (self.lo, self.hi) if v is not None)
+        m = 0
+        while True:
+            a = I.scaleb(m)
+            b = (I + 1).scaleb(m)
+            ivs.append((a, True, b - 1 if self.integer else b, self.integer))
+            if a > bound:
+                break
+            m += 1
+            if m > 400:
+                break
+        return self._side(neg, ivs)
+
+    def _side(self, neg: bool, ivs) -> bool:
+        """Magnitude intervals, mapped to values (negated for a '-' prefix)."""
+        for a, a_in, b, b_in in ivs:
+            if not neg:
+                if self._meets(a, a_in, b, b_in):
+                    return True
+            else:
+                lo, lo_in = (-b, b_in) if b is not None else (None, False)
+                if lo is None:             # unbounded below
+                    if self.lo is None:
+                        return True
+                    if self._meets(self.lo, not self.lo_ex, -a, a_in):
+                        return True
+                    continue
+                if self._meets(lo, lo_in, -a, a_in):
+                    return True
+        return False
 
 
 class SchemaPrefix:

@@ -158,3 +158,48 @@ def test_constrained_random_walk_respects_pattern():
             text += c
             assert len(text) < 200
         assert re.fullmatch("(ab|c)+-[0-9]{2,3}", json.loads(text))
+
+
+def test_numeric_ranges():
+    age = {"type": "integer", "minimum": 18, "maximum": 65}
+    assert _ok(age, "18", None) and _ok(age, "65", None) and _ok(age, "40", None)
+    assert not _ok(age, "7")                 # no completion of 7 is in [18, 65]... 70+ too big
+    assert _ok(age, "1", None)                # 18, 19 still reachable
+    assert not _ok(age, "-")
+    assert not _ok(age, "66")
+    arr = {"type": "array", "items": age}
+    assert not _ok(arr, "[1]")               # "1" cannot end below the minimum
+    assert _ok(arr, "[19,65]", True)
+    p = {"type": "number", "exclusiveMinimum": 0, "maximum": 1}
+    assert _ok(p, "0.5", None) and _ok(p, "1", None) and not _ok(p, "1.5")
+    assert not _ok({"type": "array", "items": p}, "[0]")     # 0 itself is excluded
+    assert _ok({"type": "array", "items": p}, "[0.25]", True)
+    assert not _ok(p, "2")
+    assert not _ok(p, "1e")                   # bounded numbers carry no exponent
+    neg = {"type": "number", "minimum": -10, "maximum": -2}
+    assert _ok(neg, "-3.5", None) and _ok(neg, "-10", None)
+    assert _ok(neg, "-1", None)               # -10 is still reachable
+    assert not _ok({"type": "array", "items": neg}, "[-1]")
+    assert not _ok(neg, "-11") and not _ok(neg, "3")
+
+
+def test_numeric_range_random_walk():
+    """Characters drawn at random among the allowed ones always finish on an
+    in-range number."""
+    import random
+    sch = {"type": "object", "properties": {"x": {"type": "number", "minimum": -2.5,
+                                                  "exclusiveMaximum": 40}},
+           "required": ["x"], "additionalProperties": False}
+    rng = random.Random(5)
+    alphabet = list('{}"x:-.0123456789e, ')
+    for _ in range(40):
+        s, text = SchemaPrefix(sch), ""
+        while not s.done:
+            allowed = [c for c in alphabet if s.copy().feed(c)]
+            assert allowed, text
+            c = rng.choice(allowed)
+            assert s.feed(c)
+            text += c
+            assert len(text) < 300
+        v = json.loads(text)["x"]
+        assert -2.5 <= v < 40, text
