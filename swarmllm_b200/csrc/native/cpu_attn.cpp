@@ -18,9 +18,14 @@
 // in src/inference/fast_math.rs).
 #include "cpu_attn.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <vector>
+
+// The hot loops are compiled for three x86-64 levels (AVX-512, AVX2, baseline)
+// and the loader picks the best the CPU has.
+#define SWARM_CLONES __attribute__((target_clones("arch=x86-64-v4", "arch=x86-64-v3", "default")))
 
 namespace swarm_native {
 namespace {
@@ -31,14 +36,14 @@ constexpr int kChunk = 256;
 // 15 magnitude bits moved to the float's exponent/mantissa position are the
 // value times 2^-112 (subnormal halves land on float subnormals, exactly),
 // so one multiply by 2^112 rescales; exponent 31 (inf / NaN) is patched.
-inline float half_to_float(uint16_t h) {
+__attribute__((always_inline)) inline float half_to_float(uint16_t h) {
   const uint32_t mag = (uint32_t)(h & 0x7FFF) << 13;
   float f;
   std::memcpy(&f, &mag, 4);
   f *= 5.192296858534828e33f;  // 2^112
   uint32_t bits;
   std::memcpy(&bits, &f, 4);
-  if ((h & 0x7C00) == 0x7C00) bits = 0x7F800000u | mag;  // inf / NaN keep their payload
+  bits = (h & 0x7C00) == 0x7C00 ? 0x7F800000u | mag : bits;  // inf / NaN keep their payload
   bits |= (uint32_t)(h & 0x8000) << 16;
   std::memcpy(&f, &bits, 4);
   return f;
@@ -46,13 +51,15 @@ inline float half_to_float(uint16_t h) {
 
 }  // namespace
 
-float exp_approx(float x) {
+// Selects instead of branches and rounding by adding and subtracting
+// 1.5 * 2^23 (exact to nearest for |y| < 2^22), so loops over it vectorise.
+__attribute__((always_inline)) static inline float exp_fast(float x) {
   // n = round(x / ln2), r = x - n ln2 with ln2 split into a high part with a
   // short mantissa (n * hi is exact) and the remainder (Cody and Waite), so r
   // keeps full precision however large n is; e^x = 2^n e^r, |r| <= ln2 / 2.
-  if (x < -87.3f) return 0.f;
-  if (x > 88.7f) x = 88.7f;
-  const float n = std::nearbyint(x * 1.44269504088896341f);
+  const bool under = x < -87.3f;
+  x = x < -87.3f ? -87.3f : (x > 88.7f ? 88.7f : x);
+  const float n = (x * 1.44269504088896341f + 12582912.f) - 12582912.f;
   const float r = (x - n * 0.693145751953125f) - n * 1.42860682030941723e-6f;
   float p = 1.f / 720.f;
   p = p * r + 1.f / 120.f;
@@ -64,139 +71,183 @@ float exp_approx(float x) {
   const int32_t e = ((int32_t)n + 127) << 23;
   float s;
   std::memcpy(&s, &e, 4);
-  return p * s;
+  return under ? 0.f : p * s;
 }
 
-void cpu_silu_mul(const float* g, const float* u, float* out, int64_t n, float limit, float alpha) {
-#pragma omp parallel for simd schedule(static) if (n > 65536)
-  for (int64_t i = 0; i < n; ++i) {
+float exp_approx(float x) { return exp_fast(x); }
+
+SWARM_CLONES static void silu_mul_span(const float* g, const float* u, float* out, int64_t i0,
+                                       int64_t i1, float limit, float alpha) {
+#pragma omp simd
+  for (int64_t i = i0; i < i1; ++i) {
     float a = g[i], b = u[i];
     if (limit > 0.f) {  // gpt-oss: clamped gate, clamped and shifted up, sigmoid(alpha g)
       a = a < limit ? a : limit;
       b = b < -limit ? -limit : b > limit ? limit : b;
-      out[i] = a / (1.f + exp_approx(-alpha * a)) * (b + 1.f);
+      out[i] = a / (1.f + exp_fast(-alpha * a)) * (b + 1.f);
     } else {
-      out[i] = a / (1.f + exp_approx(-a)) * b;
+      out[i] = a / (1.f + exp_fast(-a)) * b;
     }
   }
+}
+
+void cpu_silu_mul(const float* g, const float* u, float* out, int64_t n, float limit, float alpha) {
+  constexpr int64_t kSpan = 16384;
+  const int64_t spans = (n + kSpan - 1) / kSpan;
+#pragma omp parallel for schedule(static) if (spans > 4)
+  for (int64_t c = 0; c < spans; ++c)
+    silu_mul_span(g, u, out, c * kSpan, std::min(n, (c + 1) * kSpan), limit, alpha);
 }
 
 template <typename KV>
 static inline float kv_load(const KV* p, int i);
 template <>
-inline float kv_load<float>(const float* p, int i) {
+__attribute__((always_inline)) inline float kv_load<float>(const float* p, int i) {
   return p[i];
 }
 template <>
-inline float kv_load<uint16_t>(const uint16_t* p, int i) {
+__attribute__((always_inline)) inline float kv_load<uint16_t>(const uint16_t* p, int i) {
   return half_to_float(p[i]);
 }
 
+struct AttnScratch {
+  float *s, *acc, *krow, *vrow, *m, *l;
+};
+
+// One (token, KV head) pair: all the query heads of its group.  Inlined into
+// per-ISA clones (below); the OpenMP loop that hands out the pairs stays
+// outside them, since OpenMP outlines its regions before functions are cloned.
 template <typename KV>
-static void attention_t(const AttnArgs& a, const KV* kc, const KV* vc) {
-  const int N = a.n_tokens, nq = a.n_heads, nkv = a.n_kv_heads, d = a.head_dim;
+__attribute__((always_inline)) static inline void attn_task(const AttnArgs& a, const KV* kc,
+                                                            const KV* vc, int t, int g,
+                                                            AttnScratch& w) {
+  const int nq = a.n_heads, nkv = a.n_kv_heads, d = a.head_dim;
   const int rep = nq / nkv, ps = a.page_size;
-#pragma omp parallel
-  {
-    std::vector<float> s((size_t)rep * kChunk), acc((size_t)rep * d), krow(d), vrow(d);
-    std::vector<float> m(rep), l(rep);
-#pragma omp for collapse(2) schedule(dynamic)
-    for (int t = 0; t < N; ++t)
-      for (int g = 0; g < nkv; ++g) {
-        const int Lt = a.seq_lens[t];
-        const int lo = a.window > 0 && Lt > a.window ? Lt - a.window : 0;
-        const float* q = a.q + ((size_t)t * nq + (size_t)g * rep) * d;
-        const int32_t* bt = a.block_table + (size_t)t * a.max_pages;
-        const int ts = a.tree_start ? a.tree_start[t] : 0;
-        const uint64_t tm = a.tree_mask ? (uint64_t)a.tree_mask[t] : 0;
-        std::fill(acc.begin(), acc.end(), 0.f);
-        std::fill(m.begin(), m.end(), -INFINITY);
-        std::fill(l.begin(), l.end(), 0.f);
-        for (int c0 = lo; c0 < Lt; c0 += kChunk) {
-          const int nc = Lt - c0 < kChunk ? Lt - c0 : kChunk;
-          for (int j = 0; j < nc; ++j) {
-            const int key = c0 + j;
-            bool vis = true;
-            if (a.tree_mask) {
-              const int rel = key - ts;
-              vis = rel < 0 || (rel < 64 && ((tm >> rel) & 1));
-            }
-            if (!vis) {
-              for (int h = 0; h < rep; ++h) s[(size_t)h * kChunk + j] = -INFINITY;
-              continue;
-            }
-            const size_t off =
-                (((size_t)bt[key / ps] * nkv + g) * ps + (size_t)(key % ps)) * (size_t)d;
-            for (int i = 0; i < d; ++i) krow[i] = kv_load(kc + off, i);
-            for (int h = 0; h < rep; ++h) {
-              const float* qh = q + (size_t)h * d;
-              float dot = 0.f;
-#pragma omp simd reduction(+ : dot)
-              for (int i = 0; i < d; ++i) dot += qh[i] * krow[i];
-              dot *= a.scale;
-              if (a.softcap > 0.f) dot = a.softcap * std::tanh(dot / a.softcap);
-              s[(size_t)h * kChunk + j] = dot;
-            }
-          }
-          for (int h = 0; h < rep; ++h) {
-            float* sh = s.data() + (size_t)h * kChunk;
-            float mx = m[h];
-            for (int j = 0; j < nc; ++j) mx = sh[j] > mx ? sh[j] : mx;
-            if (mx == -INFINITY) continue;  // nothing visible yet
-            const float corr = m[h] == -INFINITY ? 0.f : exp_approx(m[h] - mx);
-            float sum = 0.f;
-#pragma omp simd reduction(+ : sum)
-            for (int j = 0; j < nc; ++j) {
-              const float p = sh[j] == -INFINITY ? 0.f : exp_approx(sh[j] - mx);
-              sh[j] = p;
-              sum += p;
-            }
-            l[h] = l[h] * corr + sum;
-            m[h] = mx;
-            float* ah = acc.data() + (size_t)h * d;
-            for (int i = 0; i < d; ++i) ah[i] *= corr;
-          }
-          for (int j = 0; j < nc; ++j) {
-            const int key = c0 + j;
-            const size_t off =
-                (((size_t)bt[key / ps] * nkv + g) * ps + (size_t)(key % ps)) * (size_t)d;
-            bool any = false;
-            for (int h = 0; h < rep; ++h) any |= s[(size_t)h * kChunk + j] > 0.f;
-            if (!any) continue;
-            for (int i = 0; i < d; ++i) vrow[i] = kv_load(vc + off, i);
-            for (int h = 0; h < rep; ++h) {
-              const float p = s[(size_t)h * kChunk + j];
-              if (p == 0.f) continue;
-              float* ah = acc.data() + (size_t)h * d;
-#pragma omp simd
-              for (int i = 0; i < d; ++i) ah[i] += p * vrow[i];
-            }
-          }
-        }
-        for (int h = 0; h < rep; ++h) {
-          float den = l[h], sc = 1.f;
-          if (a.sinks) {
-            const float sk = a.sinks[g * rep + h];
-            const float mx = m[h] > sk ? m[h] : sk;
-            sc = m[h] == -INFINITY ? 0.f : exp_approx(m[h] - mx);
-            den = l[h] * sc + exp_approx(sk - mx);
-          }
-          const float inv = den > 0.f ? sc / den : 0.f;
-          float* o = a.out + ((size_t)t * nq + (size_t)g * rep + h) * d;
-          const float* ah = acc.data() + (size_t)h * d;
-          for (int i = 0; i < d; ++i) o[i] = ah[i] * inv;
-        }
-      }
+  float *s = w.s, *acc = w.acc, *krow = w.krow, *vrow = w.vrow, *m = w.m, *l = w.l;
+  const int Lt = a.seq_lens[t];
+  const int lo = a.window > 0 && Lt > a.window ? Lt - a.window : 0;
+  const float* q = a.q + ((size_t)t * nq + (size_t)g * rep) * d;
+  const int32_t* bt = a.block_table + (size_t)t * a.max_pages;
+  const int ts = a.tree_start ? a.tree_start[t] : 0;
+  const uint64_t tm = a.tree_mask ? (uint64_t)a.tree_mask[t] : 0;
+  for (int i = 0; i < rep * d; ++i) acc[i] = 0.f;
+  for (int h = 0; h < rep; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
   }
+  for (int c0 = lo; c0 < Lt; c0 += kChunk) {
+    const int nc = Lt - c0 < kChunk ? Lt - c0 : kChunk;
+    for (int j = 0; j < nc; ++j) {
+      const int key = c0 + j;
+      bool vis = true;
+      if (a.tree_mask) {
+        const int rel = key - ts;
+        vis = rel < 0 || (rel < 64 && ((tm >> rel) & 1));
+      }
+      if (!vis) {
+        for (int h = 0; h < rep; ++h) s[(size_t)h * kChunk + j] = -INFINITY;
+        continue;
+      }
+      const size_t off =
+          (((size_t)bt[key / ps] * nkv + g) * ps + (size_t)(key % ps)) * (size_t)d;
+#pragma omp simd
+      for (int i = 0; i < d; ++i) krow[i] = kv_load(kc + off, i);
+      for (int h = 0; h < rep; ++h) {
+        const float* qh = q + (size_t)h * d;
+        float dot = 0.f;
+#pragma omp simd reduction(+ : dot)
+        for (int i = 0; i < d; ++i) dot += qh[i] * krow[i];
+        dot *= a.scale;
+        if (a.softcap > 0.f) dot = a.softcap * std::tanh(dot / a.softcap);
+        s[(size_t)h * kChunk + j] = dot;
+      }
+    }
+    for (int h = 0; h < rep; ++h) {
+      float* sh = s + (size_t)h * kChunk;
+      float mx = m[h];
+      for (int j = 0; j < nc; ++j) mx = sh[j] > mx ? sh[j] : mx;
+      if (mx == -INFINITY) continue;  // nothing visible yet
+      const float corr = m[h] == -INFINITY ? 0.f : exp_fast(m[h] - mx);
+      float sum = 0.f;
+#pragma omp simd reduction(+ : sum)
+      for (int j = 0; j < nc; ++j) {
+        const float p = sh[j] == -INFINITY ? 0.f : exp_fast(sh[j] - mx);
+        sh[j] = p;
+        sum += p;
+      }
+      l[h] = l[h] * corr + sum;
+      m[h] = mx;
+      float* ah = acc + (size_t)h * d;
+      for (int i = 0; i < d; ++i) ah[i] *= corr;
+    }
+    for (int j = 0; j < nc; ++j) {
+      const int key = c0 + j;
+      const size_t off =
+          (((size_t)bt[key / ps] * nkv + g) * ps + (size_t)(key % ps)) * (size_t)d;
+      bool any = false;
+      for (int h = 0; h < rep; ++h) any |= s[(size_t)h * kChunk + j] > 0.f;
+      if (!any) continue;
+#pragma omp simd
+      for (int i = 0; i < d; ++i) vrow[i] = kv_load(vc + off, i);
+      for (int h = 0; h < rep; ++h) {
+        const float p = s[(size_t)h * kChunk + j];
+        if (p == 0.f) continue;
+        float* ah = acc + (size_t)h * d;
+#pragma omp simd
+        for (int i = 0; i < d; ++i) ah[i] += p * vrow[i];
+      }
+    }
+  }
+  for (int h = 0; h < rep; ++h) {
+    float den = l[h], sc = 1.f;
+    if (a.sinks) {
+      const float sk = a.sinks[g * rep + h];
+      const float mx = m[h] > sk ? m[h] : sk;
+      sc = m[h] == -INFINITY ? 0.f : exp_fast(m[h] - mx);
+      den = l[h] * sc + exp_fast(sk - mx);
+    }
+    const float inv = den > 0.f ? sc / den : 0.f;
+    float* o = a.out + ((size_t)t * nq + (size_t)g * rep + h) * d;
+    const float* ah = acc + (size_t)h * d;
+    for (int i = 0; i < d; ++i) o[i] = ah[i] * inv;
+  }
+}
+
+SWARM_CLONES static void attn_task_f16(const AttnArgs& a, const uint16_t* k, const uint16_t* v,
+                                       int t, int g, AttnScratch& w) {
+  attn_task(a, k, v, t, g, w);
+}
+
+SWARM_CLONES static void attn_task_f32(const AttnArgs& a, const float* k, const float* v, int t,
+                                       int g, AttnScratch& w) {
+  attn_task(a, k, v, t, g, w);
 }
 
 int cpu_paged_attention(const AttnArgs& a, const void* k_cache, const void* v_cache,
                         bool kv_fp16) {
   if (a.n_heads % a.n_kv_heads != 0 || a.head_dim <= 0 || a.page_size <= 0) return -1;
-  if (kv_fp16)
-    attention_t(a, static_cast<const uint16_t*>(k_cache), static_cast<const uint16_t*>(v_cache));
-  else
-    attention_t(a, static_cast<const float*>(k_cache), static_cast<const float*>(v_cache));
+  const int rep = a.n_heads / a.n_kv_heads, d = a.head_dim;
+#pragma omp parallel
+  {
+    std::vector<float> buf((size_t)rep * kChunk + (size_t)rep * d + 2 * (size_t)d + 2 * rep);
+    AttnScratch w;
+    w.s = buf.data();
+    w.acc = w.s + (size_t)rep * kChunk;
+    w.krow = w.acc + (size_t)rep * d;
+    w.vrow = w.krow + d;
+    w.m = w.vrow + d;
+    w.l = w.m + rep;
+#pragma omp for collapse(2) schedule(dynamic)
+    for (int t = 0; t < a.n_tokens; ++t)
+      for (int g = 0; g < a.n_kv_heads; ++g) {
+        if (kv_fp16)
+          attn_task_f16(a, static_cast<const uint16_t*>(k_cache),
+                        static_cast<const uint16_t*>(v_cache), t, g, w);
+        else
+          attn_task_f32(a, static_cast<const float*>(k_cache), static_cast<const float*>(v_cache),
+                        t, g, w);
+      }
+  }
   return 0;
 }
 
@@ -204,45 +255,56 @@ int cpu_paged_attention(const AttnArgs& a, const void* k_cache, const void* v_ca
 
 namespace swarm_native {
 
+// One value head's recurrence over the T rows (per-ISA clones; the OpenMP
+// loop over heads stays outside them).
+SWARM_CLONES static void delta_head(const float* q, const float* k, const float* v,
+                                    const float* g, const float* beta, float* state, float* out,
+                                    int T, int nk, int nv, int dk, int dv, int h, float* kv,
+                                    float* d) {
+  const int rep = nv / nk;
+  float* S = state + (size_t)h * dk * dv;
+  const int kh = h / rep;
+  for (int t = 0; t < T; ++t) {
+    const float* kt = k + ((size_t)t * nk + kh) * dk;
+    const float* qt = q + ((size_t)t * nk + kh) * dk;
+    const float* vt = v + ((size_t)t * nv + h) * dv;
+    const float decay = exp_fast(g[(size_t)t * nv + h]);
+    const float b = beta[(size_t)t * nv + h];
+    for (int j = 0; j < dv; ++j) kv[j] = 0.f;
+    for (int i = 0; i < dk; ++i) {  // decay the state and read it at k in one pass
+      float* Si = S + (size_t)i * dv;
+      const float ki = kt[i];
+#pragma omp simd
+      for (int j = 0; j < dv; ++j) {
+        Si[j] *= decay;
+        kv[j] += Si[j] * ki;
+      }
+    }
+#pragma omp simd
+    for (int j = 0; j < dv; ++j) d[j] = b * (vt[j] - kv[j]);
+    float* o = out + ((size_t)t * nv + h) * dv;
+    for (int j = 0; j < dv; ++j) o[j] = 0.f;
+    for (int i = 0; i < dk; ++i) {  // rank-1 update, then read at q
+      float* Si = S + (size_t)i * dv;
+      const float ki = kt[i], qi = qt[i];
+#pragma omp simd
+      for (int j = 0; j < dv; ++j) {
+        Si[j] += ki * d[j];
+        o[j] += Si[j] * qi;
+      }
+    }
+  }
+}
+
 void cpu_delta_rule(const float* q, const float* k, const float* v, const float* g,
                     const float* beta, float* state, float* out, int T, int nk, int nv, int dk,
                     int dv) {
-  const int rep = nv / nk;
-#pragma omp parallel for schedule(static)
-  for (int h = 0; h < nv; ++h) {
-    float* S = state + (size_t)h * dk * dv;
+#pragma omp parallel
+  {
     std::vector<float> kv(dv), d(dv);
-    const int kh = h / rep;
-    for (int t = 0; t < T; ++t) {
-      const float* kt = k + ((size_t)t * nk + kh) * dk;
-      const float* qt = q + ((size_t)t * nk + kh) * dk;
-      const float* vt = v + ((size_t)t * nv + h) * dv;
-      const float decay = std::exp(g[(size_t)t * nv + h]);
-      const float b = beta[(size_t)t * nv + h];
-      std::fill(kv.begin(), kv.end(), 0.f);
-      for (int i = 0; i < dk; ++i) {  // decay the state and read it at k in one pass
-        float* Si = S + (size_t)i * dv;
-        const float ki = kt[i];
-#pragma omp simd
-        for (int j = 0; j < dv; ++j) {
-          Si[j] *= decay;
-          kv[j] += Si[j] * ki;
-        }
-      }
-#pragma omp simd
-      for (int j = 0; j < dv; ++j) d[j] = b * (vt[j] - kv[j]);
-      float* o = out + ((size_t)t * nv + h) * dv;
-      std::fill(o, o + dv, 0.f);
-      for (int i = 0; i < dk; ++i) {  // rank-1 update, then read at q
-        float* Si = S + (size_t)i * dv;
-        const float ki = kt[i], qi = qt[i];
-#pragma omp simd
-        for (int j = 0; j < dv; ++j) {
-          Si[j] += ki * d[j];
-          o[j] += Si[j] * qi;
-        }
-      }
-    }
+#pragma omp for schedule(static)
+    for (int h = 0; h < nv; ++h)
+      delta_head(q, k, v, g, beta, state, out, T, nk, nv, dk, dv, h, kv.data(), d.data());
   }
 }
 
