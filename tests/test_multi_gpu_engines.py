@@ -33,15 +33,16 @@ def _cfg():
 
 
 def _hybrid_cfg():
-    """Qwen3-Next-like: gated DeltaNet + gated attention (2 KV heads: replicated
-    at TP4), 8 experts top-2 with a shared expert."""
+    """Qwen3-Next-like: gated DeltaNet (4 key heads: whole heads per rank up to
+    TP4) + gated attention (2 KV heads: replicated at TP4), 8 experts top-2
+    with a shared expert."""
     from swarmllm_b200.models.config import ModelConfig
     return ModelConfig(name="t-hybrid", arch="qwen3next", n_layers=4, hidden=512, n_heads=4,
                        n_kv_heads=2, head_dim=256, ffn=512, vocab=1024, rope_theta=1e7,
                        rope_neox=True, rope_dim=64, rms_eps=1e-6, qk_norm=True,
                        attn_output_gate=True, n_experts=8, n_experts_used=2, expert_ffn=256,
                        shared_expert_ffn=512, moe_softmax_after_topk=True,
-                       full_attn_interval=4, ssm_k_heads=2, ssm_v_heads=8, ssm_head_dim=128,
+                       full_attn_interval=4, ssm_k_heads=4, ssm_v_heads=8, ssm_head_dim=128,
                        ssm_conv_kernel=4, weight_qtype="Q4_K", embed_qtype="F16",
                        output_qtype="Q4_K", expert_qtype="Q4_K")
 
@@ -148,8 +149,18 @@ def _spawn(fn, world, timeout=600):
     procs = [ctx.Process(target=fn, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
+    import queue
+    import time as _time
     try:
-        got = q.get(timeout=timeout)
+        deadline = _time.time() + timeout
+        while True:   # fail as soon as a rank dies instead of waiting out the timeout
+            try:
+                got = q.get(timeout=5)
+                break
+            except queue.Empty:
+                dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+                assert not dead, f"a rank exited with {dead} before reporting"
+                assert _time.time() < deadline, "no result before the timeout"
     finally:
         for p in procs:
             p.join(timeout=120)
