@@ -163,6 +163,8 @@ def main(argv=None):
     sub.add_parser("diagnostics")
     s = sub.add_parser("test-split")
     s.add_argument("--world", type=int, default=2)
+    s.add_argument("--native", action="store_true",
+                   help="run both sides on the native CPU kernels")
     s = sub.add_parser("shard")
     s.add_argument("gguf")
     s.add_argument("out_dir")
@@ -182,7 +184,7 @@ def main(argv=None):
         return
     if args.cmd == "test-split":
         from .parallel.split_check import split_check
-        r = split_check(world=args.world)
+        r = split_check(world=args.world, native=args.native)
         r.pop("tokens")
         print(json.dumps(r))
         sys.exit(0 if r["ok"] else 1)

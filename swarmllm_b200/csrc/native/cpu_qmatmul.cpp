@@ -1,11 +1,12 @@
 // Quantized matmul on the host CPU: out[t][r] = sum_k W[r][k] * x[t][k] with W
-// in its GGUF blocks (Q4_K, Q6_K, Q8_0), never dequantized to a float matrix.
+// in its GGUF blocks (Q4_K, Q6_K, Q8_0, Q4_0), never dequantized to a float matrix.
 //
 // The activations of every token are quantized once per call to int8 with one
 // scale per 32 values (absmax / 127, round to nearest), and each block's dot
 // product is an int8 x int8 -> int32 loop the compiler vectorises; the block
 // and sub-block scales are applied in fp32:
 //   Q8_0  sum_b d_b dx_b sum q x
+//   Q4_0  sum_b d_b dx_b sum (q - 8) x
 //   Q6_K  sum_s d sc_s dx sum (q - 32) x                (16-value sub-blocks)
 //   Q4_K  sum_j d sc_j dx_j sum q x - dmin m_j dx_j sum x  (32-value sub-blocks)
 // with the min term over the rounded activations, so the result is exactly
@@ -16,9 +17,10 @@
 // products per 32-bit lane) per token; a lane's partial sum is scaled in fp32
 // by its sub-block's scale times its activation block's scale, so all three
 // formats share one inner loop and differ only in how a block is unpacked:
-// Q4_K codes are already unsigned, Q6_K codes are used before their -32 and
-// Q8_0 codes are flipped to q + 128; the offsets come back as one correction
-// per block against the sums of the rounded activations.  This is the CPU
+// Q4_K and Q4_0 codes are already unsigned (Q4_0 before its -8), Q6_K codes
+// are used before their -32 and Q8_0 codes are flipped to q + 128; the
+// offsets come back as one correction per block against the sums of the
+// rounded activations.  This is the CPU
 // inference path of a node without a GPU (the reference's CPU kernels:
 // src/inference/split/attn_rows.rs, fast_math.rs); the fp32 PyTorch model
 // stays the numerical oracle.
@@ -160,6 +162,21 @@ void block_q6k(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* 
   }
 }
 
+// One Q4_0 block (32 values, 18 bytes: d, then value j's code in the low
+// nibble of byte j and value j + 16's in its high nibble; x = d (q - 8)).
+void block_q40(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
+  const float d = half_to_float(rd16(blk));
+  int8_t q[32];
+  for (int j = 0; j < 16; ++j) {
+    q[j] = (int8_t)((blk[2 + j] & 0xF) - 8);
+    q[16 + j] = (int8_t)((blk[2 + j] >> 4) - 8);
+  }
+  const int nb = a.K / 32;
+  for (int t = 0; t < nt; ++t)
+    acc[t] += d * a.dx[(size_t)(t0 + t) * nb + b] *
+              (float)dot_i8(q, a.q + (size_t)(t0 + t) * a.K + 32 * b, 32);
+}
+
 // One Q8_0 block (32 values, 34 bytes).
 void block_q80(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
   const float d = half_to_float(rd16(blk));
@@ -168,6 +185,15 @@ void block_q80(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* 
   for (int t = 0; t < nt; ++t)
     acc[t] += d * a.dx[(size_t)(t0 + t) * nb + b] *
               (float)dot_i8(q, a.q + (size_t)(t0 + t) * a.K + 32 * b, 32);
+}
+
+size_t row_bytes_of(int type, int K) {
+  switch (type) {
+    case kGgmlQ4_K: return (size_t)K / 256 * 144;
+    case kGgmlQ6_K: return (size_t)K / 256 * 210;
+    case kGgmlQ8_0: return (size_t)K / 32 * 34;
+    default: return (size_t)K / 32 * 18;  // Q4_0
+  }
 }
 
 // ---------------------------------------------------------------- AVX-512 VNNI
@@ -273,10 +299,30 @@ SWARM_VNNI inline void unpack_q80x8(const uint8_t* blk, Unpacked& u) {
   u.corr = _mm512_mul_ps(_mm512_castps256_ps512(_mm256_loadu_ps(d)), _mm512_set1_ps(128.f));
 }
 
-// out[t] for tokens t0..t0+nt of one weight row; FMT 0 Q4_K, 1 Q6_K, 2 Q8_0.
+// Eight Q4_0 blocks (256 values, 8 x 18 bytes): the codes as they are (0..15),
+// the offset of 8 back through the correction.
+SWARM_VNNI inline void unpack_q40x8(const uint8_t* blk, Unpacked& u) {
+  float d[8];
+  const __m128i lo4 = _mm_set1_epi8(0x0F);
+  for (int j = 0; j < 8; ++j) d[j] = half_to_float(rd16(blk + 18 * j));
+  for (int g = 0; g < 4; ++g) {
+    __m256i half[2];
+    for (int h = 0; h < 2; ++h) {
+      const __m128i v = _mm_loadu_si128(reinterpret_cast<const __m128i*>(blk + 18 * (2 * g + h) + 2));
+      const __m128i lo = _mm_and_si128(v, lo4);
+      const __m128i hi = _mm_and_si128(_mm_srli_epi16(v, 4), lo4);
+      half[h] = _mm256_inserti128_si256(_mm256_castsi128_si256(lo), hi, 1);
+    }
+    u.c[g] = _mm512_inserti64x4(_mm512_castsi256_si512(half[0]), half[1], 1);
+    u.s[g] = halves(d[2 * g], d[2 * g + 1]);
+  }
+  u.corr = _mm512_mul_ps(_mm512_castps256_ps512(_mm256_loadu_ps(d)), _mm512_set1_ps(8.f));
+}
+
+// out[t] for tokens t0..t0+nt of one weight row; FMT 0 Q4_K, 1 Q6_K, 2 Q8_0, 3 Q4_0.
 template <int FMT>
 SWARM_VNNI void row_vnni(const uint8_t* wr, int nsb, const ActsX& a, int t0, int nt, float* res) {
-  constexpr size_t SB_BYTES = FMT == 0 ? 144 : FMT == 1 ? 210 : 8 * 34;
+  constexpr size_t SB_BYTES = FMT == 0 ? 144 : FMT == 1 ? 210 : FMT == 2 ? 8 * 34 : 8 * 18;
   __m512 facc[kTT], cacc[kTT];
   for (int t = 0; t < nt; ++t) facc[t] = cacc[t] = _mm512_setzero_ps();
   // lanes 0-7 take the group's first activation scale, lanes 8-15 its second
@@ -286,7 +332,8 @@ SWARM_VNNI void row_vnni(const uint8_t* wr, int nsb, const ActsX& a, int t0, int
     Unpacked u;
     if constexpr (FMT == 0) unpack_q4k(wr + b * SB_BYTES, u);
     else if constexpr (FMT == 1) unpack_q6k(wr + b * SB_BYTES, u);
-    else unpack_q80x8(wr + b * SB_BYTES, u);
+    else if constexpr (FMT == 2) unpack_q80x8(wr + b * SB_BYTES, u);
+    else unpack_q40x8(wr + b * SB_BYTES, u);
     for (int t = 0; t < nt; ++t) {
       const size_t tt = (size_t)(t0 + t);
       const int8_t* xq = a.q + tt * K + 256 * b;
@@ -326,11 +373,12 @@ SWARM_VNNI void matmul_vnni(const uint8_t* w, int type, int rows, int K, const A
     }
   }
   const ActsX ax{acts.q, acts.dx, dxs.data(), dxs16.data(), K};
-  const size_t row_bytes = type == kGgmlQ4_K   ? (size_t)K / 256 * 144
-                           : type == kGgmlQ6_K ? (size_t)K / 256 * 210
-                                               : (size_t)K / 32 * 34;
+  const size_t row_bytes = row_bytes_of(type, K);
   const int nsb = K / 256;
-  auto* fn = type == kGgmlQ4_K ? row_vnni<0> : type == kGgmlQ6_K ? row_vnni<1> : row_vnni<2>;
+  auto* fn = type == kGgmlQ4_K   ? row_vnni<0>
+             : type == kGgmlQ6_K ? row_vnni<1>
+             : type == kGgmlQ8_0 ? row_vnni<2>
+                                 : row_vnni<3>;
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; ++r) {
     const uint8_t* wr = w + (size_t)r * row_bytes;
@@ -361,8 +409,9 @@ const char* cpu_qmatmul_isa() { return use_vnni() ? "avx512vnni" : "generic"; }
 
 int cpu_qmatmul(const uint8_t* w, int type, int rows, int K, const float* x, int T,
                 float* out) {
-  if (K % 256 != 0 && !(type == kGgmlQ8_0 && K % 32 == 0)) return -1;
-  if (type != kGgmlQ4_K && type != kGgmlQ6_K && type != kGgmlQ8_0) return -2;
+  const bool small_blocks = type == kGgmlQ8_0 || type == kGgmlQ4_0;
+  if (K % 256 != 0 && !(small_blocks && K % 32 == 0)) return -1;
+  if (type != kGgmlQ4_K && type != kGgmlQ6_K && !small_blocks) return -2;
   std::vector<int8_t> xq((size_t)T * K);
   std::vector<float> dx((size_t)T * (K / 32));
   std::vector<int32_t> sx((size_t)T * (K / 32));
@@ -374,12 +423,16 @@ int cpu_qmatmul(const uint8_t* w, int type, int rows, int K, const float* x, int
     matmul_vnni(w, type, rows, K, acts, T, out);
     return 0;
   }
-  const size_t row_bytes = type == kGgmlQ4_K   ? (size_t)K / 256 * 144
-                           : type == kGgmlQ6_K ? (size_t)K / 256 * 210
-                                               : (size_t)K / 32 * 34;
-  const int nblk = type == kGgmlQ8_0 ? K / 32 : K / 256;
-  const size_t blk_bytes = type == kGgmlQ4_K ? 144 : type == kGgmlQ6_K ? 210 : 34;
-  auto* fn = type == kGgmlQ4_K ? block_q4k : type == kGgmlQ6_K ? block_q6k : block_q80;
+  const size_t row_bytes = row_bytes_of(type, K);
+  const int nblk = small_blocks ? K / 32 : K / 256;
+  const size_t blk_bytes = type == kGgmlQ4_K   ? 144
+                           : type == kGgmlQ6_K ? 210
+                           : type == kGgmlQ8_0 ? 34
+                                               : 18;
+  auto* fn = type == kGgmlQ4_K   ? block_q4k
+             : type == kGgmlQ6_K ? block_q6k
+             : type == kGgmlQ8_0 ? block_q80
+                                 : block_q40;
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; ++r) {
     const uint8_t* wr = w + (size_t)r * row_bytes;

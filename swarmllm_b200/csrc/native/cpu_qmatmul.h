@@ -1,10 +1,11 @@
-// Quantized matmul on the host CPU over GGUF blocks (Q4_K, Q6_K, Q8_0).
+// Quantized matmul on the host CPU over GGUF blocks (Q4_K, Q6_K, Q8_0, Q4_0).
 #pragma once
 #include <cstdint>
 
 namespace swarm_native {
 
 // ggml type ids of the formats the CPU kernel reads
+constexpr int kGgmlQ4_0 = 2;
 constexpr int kGgmlQ8_0 = 8;
 constexpr int kGgmlQ4_K = 12;
 constexpr int kGgmlQ6_K = 14;

@@ -609,7 +609,7 @@ class _QWeight:
     native CPU kernel (int8 activations, csrc/native/cpu_qmatmul.cpp)."""
 
     __slots__ = ("blocks", "qtype", "rows", "K")
-    FORMATS = (Q.Q4_K, Q.Q6_K, Q.Q8_0)
+    FORMATS = (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0)
 
     def __init__(self, blocks, qtype: int, rows: int, K: int):
         self.blocks = np.ascontiguousarray(blocks.reshape(rows, -1))
@@ -664,7 +664,8 @@ class LlamaCPU:
             if not self.native:
                 return dq(name)
             t, qt, shape = source.get(name)
-            if qt in _QWeight.FORMATS and len(shape) == 2 and shape[1] % 256 == 0:
+            width = 32 if qt in (Q.Q8_0, Q.Q4_0) else 256
+            if qt in _QWeight.FORMATS and len(shape) == 2 and shape[1] % width == 0:
                 return _QWeight(t.numpy().reshape(-1), qt, shape[0], shape[1])
             return torch.from_numpy(Q.dequantize(t.numpy().reshape(-1), qt).reshape(shape)).to(dtype)
 

@@ -102,7 +102,7 @@ class AsyncPipelineEngine:
             self.sampler = DeviceSampler(self.device, per_wave_running)
         else:
             from ..models.llama import LlamaCPU
-            self.model = LlamaCPU(cfg, src, (lo, hi))
+            self.model = LlamaCPU(cfg, src, (lo, hi), native=ecfg.cpu_native)
             self.kv = PagedKVCache(hi - lo, pages + 1, cfg.n_kv_heads, cfg.head_dim, "cpu", ps,
                                    dtype=torch.float32)
             self.ctx = None

@@ -118,7 +118,7 @@ class PipelineEngine:
             self.sampler = DeviceSampler(self.device, max(ecfg.max_running, 1))
         else:
             from ..models.llama import LlamaCPU
-            self.model = LlamaCPU(cfg, src, (lo, hi))
+            self.model = LlamaCPU(cfg, src, (lo, hi), native=ecfg.cpu_native)
             self.kv = PagedKVCache(hi - lo, pages + 1, cfg.n_kv_heads, cfg.head_dim, "cpu", ps,
                                    dtype=torch.float32)
             self.ctx = None

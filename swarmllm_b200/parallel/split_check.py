@@ -23,7 +23,7 @@ def _free_port() -> int:
     return p
 
 
-def _worker(rank, world, port, out_dir, micro, n_prompts, prompt_len, gen):
+def _worker(rank, world, port, out_dir, micro, n_prompts, prompt_len, gen, native=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     import torch
@@ -35,7 +35,8 @@ def _worker(rank, world, port, out_dir, micro, n_prompts, prompt_len, gen):
     from .pipeline import PipelineEngine, init_distributed
     init_distributed("gloo", timeout_s=120)
     cfg = tiny_llama()
-    ecfg = EngineConfig(max_model_len=128, max_running=4, max_step_tokens=256, prefill_chunk=64)
+    ecfg = EngineConfig(max_model_len=128, max_running=4, max_step_tokens=256, prefill_chunk=64,
+                        cpu_native=native)
     eng = PipelineEngine(cfg, ecfg, lambda: RandomSource(cfg, seed=42), "cpu", micro_batches=micro)
     if eng.last:
         eng.record_logits = []
@@ -52,18 +53,21 @@ def _worker(rank, world, port, out_dir, micro, n_prompts, prompt_len, gen):
 
 
 def split_check(world: int = 2, micro: int = 2, n_prompts: int = 4, prompt_len: int = 32,
-                gen: int = 64) -> dict:
+                gen: int = 64, native: bool = False) -> dict:
+    """`native`: both runs on the native CPU kernels (Q4_0 weights through the
+    int8 matmul, native attention) instead of the fp32 PyTorch path."""
     import torch
     import torch.multiprocessing as mp
     with tempfile.TemporaryDirectory() as d:
         for w in (1, world):
-            mp.start_processes(_worker, args=(w, _free_port(), d, micro, n_prompts, prompt_len, gen),
+            mp.start_processes(_worker, args=(w, _free_port(), d, micro, n_prompts, prompt_len, gen,
+                                              native),
                                nprocs=w, join=True, start_method="spawn")
         t1, t2 = (torch.load(os.path.join(d, f"tokens_w{w}.pt")) for w in (1, world))
         l1, l2 = (torch.load(os.path.join(d, f"logits_w{w}.pt")) for w in (1, world))
         segs, sent = torch.load(os.path.join(d, f"stats_w{world}.pt"))
     worst = max((float((a - b).abs().max()) for a, b in zip(l1, l2)), default=float("inf"))
     ok = t1 == t2 and len(l1) == len(l2) and worst <= 1e-5
-    return {"world": world, "tokens_equal": t1 == t2, "steps": len(l1),
+    return {"world": world, "native": native, "tokens_equal": t1 == t2, "steps": len(l1),
             "first_stage_segments": segs, "first_stage_bytes_sent": sent,
             "max_logit_diff": worst, "tokens": t1, "ok": ok}

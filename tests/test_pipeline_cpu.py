@@ -23,6 +23,16 @@ def test_two_peer_split_matches_single_peer():
     assert r["first_stage_segments"] > 0 and r["first_stage_bytes_sent"] > 0
 
 
+@pytest.mark.timeout(600)
+def test_two_peer_split_native_kernels():
+    """The same split on the native CPU kernels (Q4_0 weights through the int8
+    matmul, native attention): per-row arithmetic, so the split equals one
+    process exactly."""
+    from swarmllm_b200.parallel.split_check import split_check
+    r = split_check(world=2, micro=2, gen=16, native=True)
+    assert r["native"] and r["tokens_equal"] and r["max_logit_diff"] <= 1e-5, r
+
+
 def test_stage_bounds():
     from swarmllm_b200.parallel.pipeline import stage_bounds
     b = stage_bounds(80, 8, 0.5, 1.0)
