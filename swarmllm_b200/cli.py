@@ -24,8 +24,36 @@ import sys
 import time
 
 
+def _replica_set(args):
+    """`serve --replicas N`: N whole-model engines in their own processes
+    (GPU i each, or the host CPU) behind one front scheduler."""
+    import torch
+
+    from .models.config import preset
+    from .parallel.replicas import ReplicaSet
+    from .utils.config import load_engine_config
+    if args.lora or args.mmproj or args.draft_model:
+        raise SystemExit("--replicas does not combine with --lora, --mmproj or --draft-model")
+    ecfg = load_engine_config(args.config)
+    if args.max_model_len:
+        ecfg.max_model_len = args.max_model_len
+    dev = args.device or ("cuda" if torch.cuda.is_available() else "cpu")
+    spec = {"device": "cuda" if dev.startswith("cuda") else "cpu", "ecfg": ecfg,
+            "seed": args.seed}
+    if args.gguf:
+        from .models.weights import GgufSource
+        spec["gguf"] = args.gguf
+        cfg = GgufSource(args.gguf).cfg
+    else:
+        spec["preset"] = args.model
+        cfg = preset(args.model)
+    return ReplicaSet(cfg, spec, args.replicas)
+
+
 def _engine(args):
     import torch
+    if getattr(args, "replicas", 1) > 1:
+        return _replica_set(args)
 
     from .engine import LLMEngine
     from .models.config import preset
@@ -143,6 +171,9 @@ def main(argv=None):
                                 "(discarded when written by another build or model)")
             s.add_argument("--response-store", default=None,
                            help="SQLite file for stored /v1/responses (default: in memory)")
+            s.add_argument("--replicas", type=int, default=1,
+                           help="serve with N engine replicas (one per GPU, or N CPU processes) "
+                                "behind one request router")
         if name == "generate":
             s.add_argument("--prompt", default="Hello")
             s.add_argument("--ids", default=None, help="comma-separated token ids")
@@ -213,6 +244,10 @@ def main(argv=None):
         from .serve.api import serve
         tok, tpl = _tokenizer(args, eng)
         log = get_logger("cli")
+        kv_persist = args.kv_persist if hasattr(eng, "load_prefix_cache") else None
+        if args.kv_persist and not kv_persist:
+            log.warning("--kv-persist is ignored with --replicas")
+        args.kv_persist = kv_persist
         if args.kv_persist and eng.ecfg.prefix_cache:
             log.info("prefix cache: %d tokens loaded from %s",
                      eng.load_prefix_cache(args.kv_persist), args.kv_persist)
@@ -225,6 +260,8 @@ def main(argv=None):
             if args.kv_persist and eng.ecfg.prefix_cache:
                 log.info("prefix cache: %d tokens saved to %s",
                          eng.save_prefix_cache(args.kv_persist), args.kv_persist)
+            if hasattr(eng, "close"):
+                eng.close()
         return
     from .engine.sampling import SamplingParams
     if args.cmd == "chat":

@@ -199,6 +199,15 @@ class AsyncEngine:
                 s = self._subs.get(rid)
                 if s is None:
                     continue
+                if tok is None:  # the engine could not serve it (e.g. its replica failed)
+                    err = getattr(eng, "error_of", lambda r: None)(rid) or "request failed"
+                    self._subs.pop(rid, None)
+                    try:
+                        eng.release(rid)
+                    except Exception:
+                        pass
+                    s.loop.call_soon_threadsafe(s.q.put_nowait, ("error", err))
+                    continue
                 s.loop.call_soon_threadsafe(s.q.put_nowait, ("token", tok))
                 if fin:
                     self._finish(rid, "length")
