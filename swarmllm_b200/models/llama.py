@@ -608,12 +608,13 @@ class _QWeight:
     """Rows of a GGUF-quantized weight kept in their blocks, multiplied by the
     native CPU kernel (int8 activations, csrc/native/cpu_qmatmul.cpp)."""
 
-    __slots__ = ("blocks", "qtype", "rows", "K")
+    __slots__ = ("blocks", "qtype", "rows", "K", "expert_rows")
     FORMATS = (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0)
 
     def __init__(self, blocks, qtype: int, rows: int, K: int):
         self.blocks = np.ascontiguousarray(blocks.reshape(rows, -1))
         self.qtype, self.rows, self.K = qtype, rows, K
+        self.expert_rows = 0
 
     def __getitem__(self, sl: slice) -> "_QWeight":
         part = self.blocks[sl]
@@ -652,6 +653,7 @@ class LlamaCPU:
         self.kv_off = 0 if kv_layer_offset is None else kv_layer_offset
         self.dtype = dtype
         self.native = bool(native) and dtype == torch.float32
+        self._source = source
         self.nk_loc, self.nv_loc = cfg.ssm_k_heads, cfg.ssm_v_heads
 
         def dq(name):
@@ -734,15 +736,15 @@ class LlamaCPU:
             gpt = cfg.arch == "gpt-oss"
             L.wr = dq(b + "ffn_gate_inp.weight")
             L.br = dq(b + "ffn_gate_inp.bias") if gpt else None
-            L.eg, L.eu, L.ed = (dq(b + n) for n in ("ffn_gate_exps.weight", "ffn_up_exps.weight",
-                                                     "ffn_down_exps.weight"))
+            L.eg, L.eu, L.ed = (self._experts(b + n, dq) for n in (
+                "ffn_gate_exps.weight", "ffn_up_exps.weight", "ffn_down_exps.weight"))
             L.ebg = dq(b + "ffn_gate_exps.bias") if gpt else None
             L.ebu = dq(b + "ffn_up_exps.bias") if gpt else None
             L.ebd = dq(b + "ffn_down_exps.bias") if gpt else None
             L.sel_b = dq(b + "exp_probs_b.bias") if cfg.moe_gating == "sigmoid" else None
             L.sg = L.sgi = None
             if cfg.shared_expert_ffn:
-                L.sg, L.su, L.sd = (dq(b + n) for n in ("ffn_gate_shexp.weight", "ffn_up_shexp.weight",
+                L.sg, L.su, L.sd = (lw(b + n) for n in ("ffn_gate_shexp.weight", "ffn_up_shexp.weight",
                                                          "ffn_down_shexp.weight"))
                 if cfg.shared_expert_gated:
                     L.sgi = dq(b + "ffn_gate_inp_shexp.weight")
@@ -751,6 +753,28 @@ class LlamaCPU:
             L.wg, L.wu, L.wd = gu[:cfg.ffn], gu[cfg.ffn:], lw(b + "ffn_down.weight")
         else:
             L.wg, L.wu, L.wd = lw(b + "ffn_gate.weight"), lw(b + "ffn_up.weight"), lw(b + "ffn_down.weight")
+
+    def _experts(self, name, dq):
+        """An expert stack [E, rows, K]: in native mode and a native format, one
+        quantized [E * rows, K] matrix (expert e = its rows e*rows..), else the
+        dequantized tensor."""
+        if self.native:
+            t, qt, shape = self._source.get(name)
+            E, R, K = shape
+            width = 32 if qt in (Q.Q8_0, Q.Q4_0) else 256
+            if qt in _QWeight.FORMATS and K % width == 0:
+                W = _QWeight(t.numpy().reshape(-1), qt, E * R, K)
+                W.expert_rows = R
+                return W
+        return dq(name)
+
+    @staticmethod
+    def _expert(W, e):
+        """Expert e's [rows, K] weight of a stack from `_experts`."""
+        if isinstance(W, _QWeight):
+            R = W.expert_rows
+            return W[e * R:(e + 1) * R]
+        return W[e]
 
     @staticmethod
     def _mm(x, W):
@@ -926,13 +950,14 @@ class LlamaCPU:
             rows = sel.any(1).nonzero().flatten()
             we = (w * sel).sum(1)[rows]
             xs = x[rows]
-            g = xs @ L.eg[e].T + (L.ebg[e] if L.ebg is not None else 0)
-            u = xs @ L.eu[e].T + (L.ebu[e] if L.ebu is not None else 0)
-            o = self._act(g, u) @ L.ed[e].T + (L.ebd[e] if L.ebd is not None else 0)
+            mm, ex = self._mm, self._expert
+            g = mm(xs, ex(L.eg, e)) + (L.ebg[e] if L.ebg is not None else 0)
+            u = mm(xs, ex(L.eu, e)) + (L.ebu[e] if L.ebu is not None else 0)
+            o = mm(self._act(g, u), ex(L.ed, e)) + (L.ebd[e] if L.ebd is not None else 0)
             y[rows] += we[:, None] * o
         if L.sg is not None:
             gate = torch.sigmoid(x @ L.sgi)[:, None] if L.sgi is not None else 1.0
-            y = y + gate * ((torch.nn.functional.silu(x @ L.sg.T) * (x @ L.su.T)) @ L.sd.T)
+            y = y + gate * self._mm(self._glu(self._mm(x, L.sg), self._mm(x, L.su)), L.sd)
         return y
 
     def forward(self, b: StepBatch, kv: PagedKVCache, ctx=None, h_in=None) -> torch.Tensor:

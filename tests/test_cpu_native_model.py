@@ -29,7 +29,8 @@ def _run(m, cfg, T=40):
 
 
 @pytest.mark.parametrize("fam,qtype", [("mistral", "Q4_K"), ("qwen3", "Q6_K"), ("phi3", "Q8_0"),
-                                       ("gemma2", "Q4_K"), ("glm4", "Q8_0")])
+                                       ("gemma2", "Q4_K"), ("glm4", "Q8_0"), ("qwen2moe", "Q4_K"),
+                                       ("qwen3moe", "Q8_0"), ("glm4moe", "Q4_K")])
 def test_native_cpu_path_matches_oracle(fam, qtype):
     from swarmllm_b200.models.llama import LlamaCPU, _QWeight
     from swarmllm_b200.models.weights import RandomSource
@@ -39,6 +40,9 @@ def test_native_cpu_path_matches_oracle(fam, qtype):
     src = RandomSource(cfg, seed=3)
     ref, nat = LlamaCPU(cfg, src), LlamaCPU(cfg, src, native=True)
     assert isinstance(nat.layers[0].wo, _QWeight)
+    if cfg.n_experts:
+        moe = [L for L in nat.layers if L.moe]
+        assert moe and isinstance(moe[0].eg, _QWeight) and moe[0].eg.expert_rows == cfg.expert_ffn
     assert isinstance(nat.head, _QWeight) != cfg.tie_embeddings   # a tied F16 head stays dense
     for r, n in zip(_run(ref, cfg), _run(nat, cfg)):
         rel = (n - r).norm() / r.norm()
