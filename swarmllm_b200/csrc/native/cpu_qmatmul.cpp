@@ -1,5 +1,6 @@
 // Quantized matmul on the host CPU: out[t][r] = sum_k W[r][k] * x[t][k] with W
-// in its GGUF blocks (Q4_K, Q6_K, Q8_0, Q4_0), never dequantized to a float matrix.
+// in its GGUF blocks (Q4_K, Q6_K, Q8_0, Q4_0, IQ4_NL, MXFP4), never dequantized
+// to a float matrix.
 //
 // The activations of every token are quantized once per call to int8 with one
 // scale per 32 values (absmax / 127, round to nearest), and each block's dot
@@ -7,6 +8,7 @@
 // and sub-block scales are applied in fp32:
 //   Q8_0  sum_b d_b dx_b sum q x
 //   Q4_0  sum_b d_b dx_b sum (q - 8) x
+//   IQ4_NL / MXFP4  sum_b s_b dx_b sum book[q] x  (s_b: fp16 d, or 2^(e - 128))
 //   Q6_K  sum_s d sc_s dx sum (q - 32) x                (16-value sub-blocks)
 //   Q4_K  sum_j d sc_j dx_j sum q x - dmin m_j dx_j sum x  (32-value sub-blocks)
 // with the min term over the rounded activations, so the result is exactly
@@ -177,6 +179,36 @@ void block_q40(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* 
               (float)dot_i8(q, a.q + (size_t)(t0 + t) * a.K + 32 * b, 32);
 }
 
+// The 4-bit code books of the table formats (value = scale * code).
+constexpr int8_t kIq4Code[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
+                                 1,    13,   25,  38,  53,  69,  89,  113};
+// MXFP4: E2M1 values doubled (0, 0.5, ..., 6 -> 0, 1, ..., 12); the E8M0 block
+// scale 2^(e - 128) then gives the value.
+constexpr int8_t kMxfp4Code[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+
+// Block scale of a table format: fp16 d (IQ4_NL) or E8M0 exponent (MXFP4).
+inline float lut_scale(int type, const uint8_t* blk) {
+  return type == kGgmlIQ4_NL ? half_to_float(rd16(blk)) : std::ldexp(1.f, (int)blk[0] - 128);
+}
+
+// One IQ4_NL (18 bytes) or MXFP4 (17 bytes) block of 32 values: codes in the
+// nibbles as Q4_0 keeps them, mapped through the format's code book.
+template <int TYPE>
+void block_lut4(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
+  constexpr int HDR = TYPE == kGgmlIQ4_NL ? 2 : 1;
+  const int8_t* book = TYPE == kGgmlIQ4_NL ? kIq4Code : kMxfp4Code;
+  const float d = lut_scale(TYPE, blk);
+  int8_t q[32];
+  for (int j = 0; j < 16; ++j) {
+    q[j] = book[blk[HDR + j] & 0xF];
+    q[16 + j] = book[blk[HDR + j] >> 4];
+  }
+  const int nb = a.K / 32;
+  for (int t = 0; t < nt; ++t)
+    acc[t] += d * a.dx[(size_t)(t0 + t) * nb + b] *
+              (float)dot_i8(q, a.q + (size_t)(t0 + t) * a.K + 32 * b, 32);
+}
+
 // One Q8_0 block (32 values, 34 bytes).
 void block_q80(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
   const float d = half_to_float(rd16(blk));
@@ -192,7 +224,8 @@ size_t row_bytes_of(int type, int K) {
     case kGgmlQ4_K: return (size_t)K / 256 * 144;
     case kGgmlQ6_K: return (size_t)K / 256 * 210;
     case kGgmlQ8_0: return (size_t)K / 32 * 34;
-    default: return (size_t)K / 32 * 18;  // Q4_0
+    case kGgmlMXFP4: return (size_t)K / 32 * 17;
+    default: return (size_t)K / 32 * 18;  // Q4_0, IQ4_NL
   }
 }
 
@@ -319,10 +352,42 @@ SWARM_VNNI inline void unpack_q40x8(const uint8_t* blk, Unpacked& u) {
   u.corr = _mm512_mul_ps(_mm512_castps256_ps512(_mm256_loadu_ps(d)), _mm512_set1_ps(8.f));
 }
 
-// out[t] for tokens t0..t0+nt of one weight row; FMT 0 Q4_K, 1 Q6_K, 2 Q8_0, 3 Q4_0.
+// Eight IQ4_NL / MXFP4 blocks: each nibble looked up (pshufb) in the code
+// book shifted by +128, so the codes are unsigned; the +128 comes back through
+// the correction as for Q8_0.
+template <int TYPE>
+SWARM_VNNI inline void unpack_lut4x8(const uint8_t* blk, Unpacked& u) {
+  constexpr int BB = TYPE == kGgmlIQ4_NL ? 18 : 17, HDR = TYPE == kGgmlIQ4_NL ? 2 : 1;
+  const int8_t* book = TYPE == kGgmlIQ4_NL ? kIq4Code : kMxfp4Code;
+  alignas(16) uint8_t ub[16];
+  for (int i = 0; i < 16; ++i) ub[i] = (uint8_t)(book[i] + 128);
+  const __m128i table = _mm_load_si128(reinterpret_cast<const __m128i*>(ub));
+  const __m128i lo4 = _mm_set1_epi8(0x0F);
+  float d[8];
+  for (int j = 0; j < 8; ++j) d[j] = lut_scale(TYPE, blk + BB * j);
+  for (int g = 0; g < 4; ++g) {
+    __m256i half[2];
+    for (int h = 0; h < 2; ++h) {
+      const __m128i v = _mm_loadu_si128(reinterpret_cast<const __m128i*>(blk + BB * (2 * g + h) + HDR));
+      const __m128i lo = _mm_shuffle_epi8(table, _mm_and_si128(v, lo4));
+      const __m128i hi = _mm_shuffle_epi8(table, _mm_and_si128(_mm_srli_epi16(v, 4), lo4));
+      half[h] = _mm256_inserti128_si256(_mm256_castsi128_si256(lo), hi, 1);
+    }
+    u.c[g] = _mm512_inserti64x4(_mm512_castsi256_si512(half[0]), half[1], 1);
+    u.s[g] = halves(d[2 * g], d[2 * g + 1]);
+  }
+  u.corr = _mm512_mul_ps(_mm512_castps256_ps512(_mm256_loadu_ps(d)), _mm512_set1_ps(128.f));
+}
+
+// out[t] for tokens t0..t0+nt of one weight row; FMT 0 Q4_K, 1 Q6_K, 2 Q8_0,
+// 3 Q4_0, 4 IQ4_NL, 5 MXFP4.
 template <int FMT>
 SWARM_VNNI void row_vnni(const uint8_t* wr, int nsb, const ActsX& a, int t0, int nt, float* res) {
-  constexpr size_t SB_BYTES = FMT == 0 ? 144 : FMT == 1 ? 210 : FMT == 2 ? 8 * 34 : 8 * 18;
+  constexpr size_t SB_BYTES = FMT == 0   ? 144
+                              : FMT == 1 ? 210
+                              : FMT == 2 ? 8 * 34
+                              : FMT == 5 ? 8 * 17
+                                         : 8 * 18;
   __m512 facc[kTT], cacc[kTT];
   for (int t = 0; t < nt; ++t) facc[t] = cacc[t] = _mm512_setzero_ps();
   // lanes 0-7 take the group's first activation scale, lanes 8-15 its second
@@ -333,7 +398,9 @@ SWARM_VNNI void row_vnni(const uint8_t* wr, int nsb, const ActsX& a, int t0, int
     if constexpr (FMT == 0) unpack_q4k(wr + b * SB_BYTES, u);
     else if constexpr (FMT == 1) unpack_q6k(wr + b * SB_BYTES, u);
     else if constexpr (FMT == 2) unpack_q80x8(wr + b * SB_BYTES, u);
-    else unpack_q40x8(wr + b * SB_BYTES, u);
+    else if constexpr (FMT == 3) unpack_q40x8(wr + b * SB_BYTES, u);
+    else if constexpr (FMT == 4) unpack_lut4x8<kGgmlIQ4_NL>(wr + b * SB_BYTES, u);
+    else unpack_lut4x8<kGgmlMXFP4>(wr + b * SB_BYTES, u);
     for (int t = 0; t < nt; ++t) {
       const size_t tt = (size_t)(t0 + t);
       const int8_t* xq = a.q + tt * K + 256 * b;
@@ -375,10 +442,12 @@ SWARM_VNNI void matmul_vnni(const uint8_t* w, int type, int rows, int K, const A
   const ActsX ax{acts.q, acts.dx, dxs.data(), dxs16.data(), K};
   const size_t row_bytes = row_bytes_of(type, K);
   const int nsb = K / 256;
-  auto* fn = type == kGgmlQ4_K   ? row_vnni<0>
-             : type == kGgmlQ6_K ? row_vnni<1>
-             : type == kGgmlQ8_0 ? row_vnni<2>
-                                 : row_vnni<3>;
+  auto* fn = type == kGgmlQ4_K     ? row_vnni<0>
+             : type == kGgmlQ6_K   ? row_vnni<1>
+             : type == kGgmlQ8_0   ? row_vnni<2>
+             : type == kGgmlQ4_0   ? row_vnni<3>
+             : type == kGgmlIQ4_NL ? row_vnni<4>
+                                   : row_vnni<5>;
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; ++r) {
     const uint8_t* wr = w + (size_t)r * row_bytes;
@@ -409,7 +478,8 @@ const char* cpu_qmatmul_isa() { return use_vnni() ? "avx512vnni" : "generic"; }
 
 int cpu_qmatmul(const uint8_t* w, int type, int rows, int K, const float* x, int T,
                 float* out) {
-  const bool small_blocks = type == kGgmlQ8_0 || type == kGgmlQ4_0;
+  const bool small_blocks = type == kGgmlQ8_0 || type == kGgmlQ4_0 || type == kGgmlIQ4_NL ||
+                            type == kGgmlMXFP4;
   if (K % 256 != 0 && !(small_blocks && K % 32 == 0)) return -1;
   if (type != kGgmlQ4_K && type != kGgmlQ6_K && !small_blocks) return -2;
   std::vector<int8_t> xq((size_t)T * K);
@@ -428,11 +498,14 @@ int cpu_qmatmul(const uint8_t* w, int type, int rows, int K, const float* x, int
   const size_t blk_bytes = type == kGgmlQ4_K   ? 144
                            : type == kGgmlQ6_K ? 210
                            : type == kGgmlQ8_0 ? 34
+                           : type == kGgmlMXFP4 ? 17
                                                : 18;
-  auto* fn = type == kGgmlQ4_K   ? block_q4k
-             : type == kGgmlQ6_K ? block_q6k
-             : type == kGgmlQ8_0 ? block_q80
-                                 : block_q40;
+  auto* fn = type == kGgmlQ4_K     ? block_q4k
+             : type == kGgmlQ6_K   ? block_q6k
+             : type == kGgmlQ8_0   ? block_q80
+             : type == kGgmlQ4_0   ? block_q40
+             : type == kGgmlIQ4_NL ? block_lut4<kGgmlIQ4_NL>
+                                   : block_lut4<kGgmlMXFP4>;
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; ++r) {
     const uint8_t* wr = w + (size_t)r * row_bytes;

@@ -1,4 +1,5 @@
-// Quantized matmul on the host CPU over GGUF blocks (Q4_K, Q6_K, Q8_0, Q4_0).
+// Quantized matmul on the host CPU over GGUF blocks (Q4_K, Q6_K, Q8_0, Q4_0,
+// IQ4_NL, MXFP4).
 #pragma once
 #include <cstdint>
 
@@ -9,6 +10,8 @@ constexpr int kGgmlQ4_0 = 2;
 constexpr int kGgmlQ8_0 = 8;
 constexpr int kGgmlQ4_K = 12;
 constexpr int kGgmlQ6_K = 14;
+constexpr int kGgmlIQ4_NL = 20;
+constexpr int kGgmlMXFP4 = 39;
 
 // out [T, rows] = x [T, K] . W^T, W = `rows` rows of GGUF blocks of `type`.
 // Returns 0, or < 0 for an unsupported type or K.

@@ -609,7 +609,8 @@ class _QWeight:
     native CPU kernel (int8 activations, csrc/native/cpu_qmatmul.cpp)."""
 
     __slots__ = ("blocks", "qtype", "rows", "K", "expert_rows")
-    FORMATS = (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0)
+    FORMATS = (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.MXFP4)
+    SMALL = (Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.MXFP4)      # 32-value blocks: any K % 32
 
     def __init__(self, blocks, qtype: int, rows: int, K: int):
         self.blocks = np.ascontiguousarray(blocks.reshape(rows, -1))
@@ -666,7 +667,7 @@ class LlamaCPU:
             if not self.native:
                 return dq(name)
             t, qt, shape = source.get(name)
-            width = 32 if qt in (Q.Q8_0, Q.Q4_0) else 256
+            width = 32 if qt in _QWeight.SMALL else 256
             if qt in _QWeight.FORMATS and len(shape) == 2 and shape[1] % width == 0:
                 return _QWeight(t.numpy().reshape(-1), qt, shape[0], shape[1])
             return torch.from_numpy(Q.dequantize(t.numpy().reshape(-1), qt).reshape(shape)).to(dtype)
@@ -761,7 +762,7 @@ class LlamaCPU:
         if self.native:
             t, qt, shape = self._source.get(name)
             E, R, K = shape
-            width = 32 if qt in (Q.Q8_0, Q.Q4_0) else 256
+            width = 32 if qt in _QWeight.SMALL else 256
             if qt in _QWeight.FORMATS and K % width == 0:
                 W = _QWeight(t.numpy().reshape(-1), qt, E * R, K)
                 W.expert_rows = R

@@ -101,3 +101,23 @@ def test_native_hybrid_model_matches_oracle():
         outs.append(torch.cat(res))
     rel = (outs[1] - outs[0]).norm() / outs[0].norm()
     assert rel < 3e-2, rel
+
+
+def test_native_gpt_oss_mxfp4_experts():
+    """gpt-oss: bf16 attention with sinks and a window (dequantized), MXFP4
+    experts with biases and the clamped SwiGLU through the native matmul."""
+    from swarmllm_b200.models.config import ModelConfig
+    from swarmllm_b200.models.llama import LlamaCPU, _QWeight
+    from swarmllm_b200.models.weights import RandomSource
+    cfg = ModelConfig(name="t-oss", arch="gpt-oss", n_layers=2, hidden=256, n_heads=8,
+                      n_kv_heads=2, head_dim=64, ffn=128, vocab=1024, rope_theta=150000.0,
+                      rope_neox=True, attn_bias=True, attn_sinks=True, sliding_window=16,
+                      swa_every=2, n_experts=8, n_experts_used=4, expert_ffn=128,
+                      swiglu_limit=7.0, weight_qtype="BF16", embed_qtype="BF16",
+                      output_qtype="BF16", expert_qtype="MXFP4")
+    src = RandomSource(cfg, seed=4)
+    ref, nat = LlamaCPU(cfg, src), LlamaCPU(cfg, src, native=True)
+    assert isinstance(nat.layers[0].eg, _QWeight) and isinstance(nat.layers[0].ed, _QWeight)
+    for r, n in zip(_run(ref, cfg), _run(nat, cfg)):
+        rel = (n - r).norm() / r.norm()
+        assert rel < 3e-2, rel

@@ -22,7 +22,7 @@ def _round_like_kernel(x: np.ndarray) -> np.ndarray:
     return (q * (amax / np.float32(127))).reshape(T, K).astype(np.float32)
 
 
-@pytest.mark.parametrize("qtype", [Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0])
+@pytest.mark.parametrize("qtype", [Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.MXFP4])
 @pytest.mark.parametrize("T", [1, 3])
 def test_cpu_qmatmul_matches_dequantized(qtype, T):
     rng = np.random.default_rng(qtype * 10 + T)
@@ -44,7 +44,7 @@ def test_cpu_qmatmul_rejects_bad_shapes():
     with pytest.raises(ValueError):
         _native.cpu_qmatmul(w, Q.Q4_K, 4, 256, np.zeros((1, 128), np.float32))
     with pytest.raises(ValueError):
-        _native.cpu_qmatmul(w, Q.IQ4_NL, 4, 256, np.zeros((1, 256), np.float32))
+        _native.cpu_qmatmul(w, Q.IQ4_XS, 4, 256, np.zeros((1, 256), np.float32))
 
 
 def test_cpu_qmatmul_generic_path_agrees():
@@ -60,7 +60,7 @@ def test_cpu_qmatmul_generic_path_agrees():
         "rng = np.random.default_rng(7)\n"
         "x = rng.standard_normal((5, 512), dtype=np.float32)\n"
         "outs = []\n"
-        "for qt in (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0):\n"
+        "for qt in (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.MXFP4):\n"
         "    w = Q.random_quantized(40, 512, qt, rng=rng)\n"
         "    outs.append(_native.cpu_qmatmul(w, qt, 40, 512, x))\n"
         "np.save(__import__('sys').argv[1], np.stack(outs))\n"
@@ -84,7 +84,7 @@ def test_cpu_qmatmul_generic_path_agrees():
         assert np.abs(res["generic"] - res["auto"]).max() <= 1e-5 * scale
 
 
-@pytest.mark.parametrize("qtype", [Q.Q8_0, Q.Q4_0])
+@pytest.mark.parametrize("qtype", [Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.MXFP4])
 def test_cpu_qmatmul_small_blocks_any_width(qtype):
     """32-value block formats take any K that is a multiple of 32 (the
     portable path runs when K is not a multiple of 256)."""
