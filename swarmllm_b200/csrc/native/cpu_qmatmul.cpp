@@ -1,6 +1,6 @@
 // Quantized matmul on the host CPU: out[t][r] = sum_k W[r][k] * x[t][k] with W
-// in its GGUF blocks (Q4_K, Q6_K, Q8_0, Q4_0, IQ4_NL, MXFP4), never dequantized
-// to a float matrix.
+// in its GGUF blocks (Q4_K, Q6_K, Q8_0, Q4_0, IQ4_NL, IQ4_XS, MXFP4), never
+// dequantized to a float matrix.
 //
 // The activations of every token are quantized once per call to int8 with one
 // scale per 32 values (absmax / 127, round to nearest), and each block's dot
@@ -9,6 +9,7 @@
 //   Q8_0  sum_b d_b dx_b sum q x
 //   Q4_0  sum_b d_b dx_b sum (q - 8) x
 //   IQ4_NL / MXFP4  sum_b s_b dx_b sum book[q] x  (s_b: fp16 d, or 2^(e - 128))
+//   IQ4_XS  sum_j d (ls_j - 32) dx_j sum book[q] x  (32-value sub-blocks)
 //   Q6_K  sum_s d sc_s dx sum (q - 32) x                (16-value sub-blocks)
 //   Q4_K  sum_j d sc_j dx_j sum q x - dmin m_j dx_j sum x  (32-value sub-blocks)
 // with the min term over the rounded activations, so the result is exactly
@@ -209,6 +210,39 @@ void block_lut4(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float*
               (float)dot_i8(q, a.q + (size_t)(t0 + t) * a.K + 32 * b, 32);
 }
 
+// IQ4_XS sub-block scales: d * (ls_j - 32), ls_j six bits (4 low in
+// scales_l, 2 high in scales_h).
+inline void iq4xs_scales(const uint8_t* blk, float* dl) {
+  const float d = half_to_float(rd16(blk));
+  const int sh = rd16(blk + 2);
+  for (int j = 0; j < 8; ++j) {
+    const int ls = ((blk[4 + j / 2] >> (4 * (j % 2))) & 0xF) | (((sh >> (2 * j)) & 3) << 4);
+    dl[j] = d * (float)(ls - 32);
+  }
+}
+
+// One IQ4_XS block (256 values, 136 bytes: d, scales_h, scales_l[4], qs[128];
+// sub-block j's codes in qs[16j..] as Q4_0 keeps a block's).
+void block_iq4xs(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
+  float dl[8];
+  iq4xs_scales(blk, dl);
+  int8_t q[256];
+  for (int j = 0; j < 8; ++j)
+    for (int i = 0; i < 16; ++i) {
+      const uint8_t c = blk[8 + 16 * j + i];
+      q[32 * j + i] = kIq4Code[c & 0xF];
+      q[32 * j + 16 + i] = kIq4Code[c >> 4];
+    }
+  const int nb = a.K / 32;
+  for (int t = 0; t < nt; ++t) {
+    const int8_t* xq = a.q + (size_t)(t0 + t) * a.K + 256 * b;
+    const float* dx = a.dx + (size_t)(t0 + t) * nb + 8 * b;
+    float v = 0.f;
+    for (int j = 0; j < 8; ++j) v += dl[j] * dx[j] * (float)dot_i8(q + 32 * j, xq + 32 * j, 32);
+    acc[t] += v;
+  }
+}
+
 // One Q8_0 block (32 values, 34 bytes).
 void block_q80(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
   const float d = half_to_float(rd16(blk));
@@ -225,6 +259,7 @@ size_t row_bytes_of(int type, int K) {
     case kGgmlQ6_K: return (size_t)K / 256 * 210;
     case kGgmlQ8_0: return (size_t)K / 32 * 34;
     case kGgmlMXFP4: return (size_t)K / 32 * 17;
+    case kGgmlIQ4_XS: return (size_t)K / 256 * 136;
     default: return (size_t)K / 32 * 18;  // Q4_0, IQ4_NL
   }
 }
@@ -379,11 +414,35 @@ SWARM_VNNI inline void unpack_lut4x8(const uint8_t* blk, Unpacked& u) {
   u.corr = _mm512_mul_ps(_mm512_castps256_ps512(_mm256_loadu_ps(d)), _mm512_set1_ps(128.f));
 }
 
+// One IQ4_XS block: its eight sub-blocks through the IQ4 code book (+128).
+SWARM_VNNI inline void unpack_iq4xs(const uint8_t* blk, Unpacked& u) {
+  alignas(16) uint8_t ub[16];
+  for (int i = 0; i < 16; ++i) ub[i] = (uint8_t)(kIq4Code[i] + 128);
+  const __m128i table = _mm_load_si128(reinterpret_cast<const __m128i*>(ub));
+  const __m128i lo4 = _mm_set1_epi8(0x0F);
+  float dl[8];
+  iq4xs_scales(blk, dl);
+  for (int g = 0; g < 4; ++g) {
+    __m256i half[2];
+    for (int h = 0; h < 2; ++h) {
+      const __m128i v =
+          _mm_loadu_si128(reinterpret_cast<const __m128i*>(blk + 8 + 16 * (2 * g + h)));
+      const __m128i lo = _mm_shuffle_epi8(table, _mm_and_si128(v, lo4));
+      const __m128i hi = _mm_shuffle_epi8(table, _mm_and_si128(_mm_srli_epi16(v, 4), lo4));
+      half[h] = _mm256_inserti128_si256(_mm256_castsi128_si256(lo), hi, 1);
+    }
+    u.c[g] = _mm512_inserti64x4(_mm512_castsi256_si512(half[0]), half[1], 1);
+    u.s[g] = halves(dl[2 * g], dl[2 * g + 1]);
+  }
+  u.corr = _mm512_mul_ps(_mm512_castps256_ps512(_mm256_loadu_ps(dl)), _mm512_set1_ps(128.f));
+}
+
 // out[t] for tokens t0..t0+nt of one weight row; FMT 0 Q4_K, 1 Q6_K, 2 Q8_0,
-// 3 Q4_0, 4 IQ4_NL, 5 MXFP4.
+// 3 Q4_0, 4 IQ4_NL, 5 MXFP4, 6 IQ4_XS.
 template <int FMT>
 SWARM_VNNI void row_vnni(const uint8_t* wr, int nsb, const ActsX& a, int t0, int nt, float* res) {
   constexpr size_t SB_BYTES = FMT == 0   ? 144
+                              : FMT == 6 ? 136
                               : FMT == 1 ? 210
                               : FMT == 2 ? 8 * 34
                               : FMT == 5 ? 8 * 17
@@ -400,7 +459,8 @@ SWARM_VNNI void row_vnni(const uint8_t* wr, int nsb, const ActsX& a, int t0, int
     else if constexpr (FMT == 2) unpack_q80x8(wr + b * SB_BYTES, u);
     else if constexpr (FMT == 3) unpack_q40x8(wr + b * SB_BYTES, u);
     else if constexpr (FMT == 4) unpack_lut4x8<kGgmlIQ4_NL>(wr + b * SB_BYTES, u);
-    else unpack_lut4x8<kGgmlMXFP4>(wr + b * SB_BYTES, u);
+    else if constexpr (FMT == 5) unpack_lut4x8<kGgmlMXFP4>(wr + b * SB_BYTES, u);
+    else unpack_iq4xs(wr + b * SB_BYTES, u);
     for (int t = 0; t < nt; ++t) {
       const size_t tt = (size_t)(t0 + t);
       const int8_t* xq = a.q + tt * K + 256 * b;
@@ -447,7 +507,8 @@ SWARM_VNNI void matmul_vnni(const uint8_t* w, int type, int rows, int K, const A
              : type == kGgmlQ8_0   ? row_vnni<2>
              : type == kGgmlQ4_0   ? row_vnni<3>
              : type == kGgmlIQ4_NL ? row_vnni<4>
-                                   : row_vnni<5>;
+             : type == kGgmlMXFP4  ? row_vnni<5>
+                                   : row_vnni<6>;
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; ++r) {
     const uint8_t* wr = w + (size_t)r * row_bytes;
@@ -481,7 +542,7 @@ int cpu_qmatmul(const uint8_t* w, int type, int rows, int K, const float* x, int
   const bool small_blocks = type == kGgmlQ8_0 || type == kGgmlQ4_0 || type == kGgmlIQ4_NL ||
                             type == kGgmlMXFP4;
   if (K % 256 != 0 && !(small_blocks && K % 32 == 0)) return -1;
-  if (type != kGgmlQ4_K && type != kGgmlQ6_K && !small_blocks) return -2;
+  if (type != kGgmlQ4_K && type != kGgmlQ6_K && type != kGgmlIQ4_XS && !small_blocks) return -2;
   std::vector<int8_t> xq((size_t)T * K);
   std::vector<float> dx((size_t)T * (K / 32));
   std::vector<int32_t> sx((size_t)T * (K / 32));
@@ -499,13 +560,15 @@ int cpu_qmatmul(const uint8_t* w, int type, int rows, int K, const float* x, int
                            : type == kGgmlQ6_K ? 210
                            : type == kGgmlQ8_0 ? 34
                            : type == kGgmlMXFP4 ? 17
+                           : type == kGgmlIQ4_XS ? 136
                                                : 18;
   auto* fn = type == kGgmlQ4_K     ? block_q4k
              : type == kGgmlQ6_K   ? block_q6k
              : type == kGgmlQ8_0   ? block_q80
              : type == kGgmlQ4_0   ? block_q40
              : type == kGgmlIQ4_NL ? block_lut4<kGgmlIQ4_NL>
-                                   : block_lut4<kGgmlMXFP4>;
+             : type == kGgmlMXFP4  ? block_lut4<kGgmlMXFP4>
+                                   : block_iq4xs;
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; ++r) {
     const uint8_t* wr = w + (size_t)r * row_bytes;

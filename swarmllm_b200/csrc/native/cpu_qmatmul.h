@@ -1,5 +1,5 @@
 // Quantized matmul on the host CPU over GGUF blocks (Q4_K, Q6_K, Q8_0, Q4_0,
-// IQ4_NL, MXFP4).
+// IQ4_NL, IQ4_XS, MXFP4).
 #pragma once
 #include <cstdint>
 
@@ -11,6 +11,7 @@ constexpr int kGgmlQ8_0 = 8;
 constexpr int kGgmlQ4_K = 12;
 constexpr int kGgmlQ6_K = 14;
 constexpr int kGgmlIQ4_NL = 20;
+constexpr int kGgmlIQ4_XS = 23;
 constexpr int kGgmlMXFP4 = 39;
 
 // out [T, rows] = x [T, K] . W^T, W = `rows` rows of GGUF blocks of `type`.

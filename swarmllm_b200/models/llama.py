@@ -609,7 +609,7 @@ class _QWeight:
     native CPU kernel (int8 activations, csrc/native/cpu_qmatmul.cpp)."""
 
     __slots__ = ("blocks", "qtype", "rows", "K", "expert_rows")
-    FORMATS = (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.MXFP4)
+    FORMATS = (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.IQ4_XS, Q.MXFP4)
     SMALL = (Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.MXFP4)      # 32-value blocks: any K % 32
 
     def __init__(self, blocks, qtype: int, rows: int, K: int):

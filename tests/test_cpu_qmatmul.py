@@ -22,7 +22,8 @@ def _round_like_kernel(x: np.ndarray) -> np.ndarray:
     return (q * (amax / np.float32(127))).reshape(T, K).astype(np.float32)
 
 
-@pytest.mark.parametrize("qtype", [Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.MXFP4])
+@pytest.mark.parametrize("qtype", [Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.IQ4_XS,
+                                   Q.MXFP4])
 @pytest.mark.parametrize("T", [1, 3])
 def test_cpu_qmatmul_matches_dequantized(qtype, T):
     rng = np.random.default_rng(qtype * 10 + T)
@@ -44,7 +45,7 @@ def test_cpu_qmatmul_rejects_bad_shapes():
     with pytest.raises(ValueError):
         _native.cpu_qmatmul(w, Q.Q4_K, 4, 256, np.zeros((1, 128), np.float32))
     with pytest.raises(ValueError):
-        _native.cpu_qmatmul(w, Q.IQ4_XS, 4, 256, np.zeros((1, 256), np.float32))
+        _native.cpu_qmatmul(w, Q.F16, 4, 256, np.zeros((1, 256), np.float32))
 
 
 def test_cpu_qmatmul_generic_path_agrees():
@@ -60,7 +61,7 @@ def test_cpu_qmatmul_generic_path_agrees():
         "rng = np.random.default_rng(7)\n"
         "x = rng.standard_normal((5, 512), dtype=np.float32)\n"
         "outs = []\n"
-        "for qt in (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.MXFP4):\n"
+        "for qt in (Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.IQ4_XS, Q.MXFP4):\n"
         "    w = Q.random_quantized(40, 512, qt, rng=rng)\n"
         "    outs.append(_native.cpu_qmatmul(w, qt, 40, 512, x))\n"
         "np.save(__import__('sys').argv[1], np.stack(outs))\n"
