@@ -163,6 +163,9 @@ def main(argv=None):
             s.add_argument("--port", type=int, default=8800)
             s.add_argument("--api-key", default=os.environ.get("SWARMLLM_API_KEY"),
                            help="require this key (Bearer or x-api-key); default: open")
+            s.add_argument("--api-key-file", default=os.environ.get("SWARMLLM_API_KEY_FILE"),
+                           help="read the key from this file; a key rotated through "
+                                "/api/admin/api-key/rotate is written back to it")
             s.add_argument("--cors-origin", action="append", default=[],
                            help="extra browser origin allowed besides localhost")
             s.add_argument("--rpm", type=int, default=0, help="requests a minute per client (0: off)")
@@ -255,7 +258,8 @@ def main(argv=None):
             serve(eng, tok, eng.cfg.name, args.host, args.port, arch=eng.cfg.arch,
                   chat_template=tpl, max_model_len=eng.ecfg.max_model_len, api_key=args.api_key,
                   cors_origins=tuple(args.cors_origin), rpm=args.rpm,
-                  store_path=args.response_store, config_path=args.config)
+                  store_path=args.response_store, config_path=args.config,
+                  api_key_file=args.api_key_file)
         finally:
             if args.kv_persist and eng.ecfg.prefix_cache:
                 log.info("prefix cache: %d tokens saved to %s",

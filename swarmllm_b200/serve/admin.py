@@ -23,14 +23,19 @@
   GET  /api/admin/schedule       scheduler state: running, waiting, preemptions, limits
   GET  /api/admin/swarm/capacity free KV tokens, GPUs, concurrency limits
   POST /api/admin/shutdown       graceful stop of a server started by serve()
+  POST /api/admin/prune-history  drop stored responses by age and/or count
+  GET  /api/admin/api-key        the key in force; POST /api-key/rotate issues a
+                                 new one, in force from the next request
+  POST /api/admin/ws-ticket      one-time 30 s ticket for /api/admin/ws?t=...
 
 Every route needs the API key when one is configured (the guards treat
 /api/admin like any other path).  Model download and Hugging Face search are
 not offered: a node here fetches nothing.
 
 Reference behaviour: src/api/admin.rs (stats, config get/update/reload,
-models, diagnostics, performance, responses, storage breakdown;
-routes at src/api/server.rs:274-330).
+models, diagnostics, performance, responses, storage breakdown, API key
+rotation at :2318 -- there in force after a restart, here at once; routes at
+src/api/server.rs:274-330); websocket tickets as src/api/middleware.rs:551.
 """
 from __future__ import annotations
 
@@ -236,6 +241,43 @@ def register(app, S, settings, config_path: str | None = None):
             rows = store.db.execute("SELECT id, created FROM responses ORDER BY created DESC LIMIT ?",
                                     (max(1, min(1000, int(limit))),)).fetchall()
         return {"data": [{"id": r[0], "created": r[1]} for r in rows]}
+
+    @app.post("/api/admin/prune-history")
+    async def prune_history(request: Request):
+        """Body {"older_than_days": d} and/or {"keep": n}: drop stored
+        /v1/responses older than d days / all but the newest n."""
+        body = await request.json() if await request.body() else {}
+        store = getattr(app.state, "response_store", None)
+        days, keep = body.get("older_than_days"), body.get("keep")
+        if days is None and keep is None:
+            raise ApiError(400, "give older_than_days and/or keep")
+        for v in (days, keep):
+            if v is not None and (not isinstance(v, (int, float)) or isinstance(v, bool) or v < 0):
+                raise ApiError(400, "older_than_days and keep must be non-negative numbers")
+        if store is None:
+            return {"removed": 0, "left": 0}
+        removed, left = store.prune(None if days is None else float(days) * 86400.0,
+                                    None if keep is None else int(keep))
+        return {"removed": removed, "left": left}
+
+    # ------------------------------------------------------------------ API key
+    @app.get("/api/admin/api-key")
+    async def api_key():
+        """The key in force (this route itself needs it when one is set)."""
+        return {"auth_required": bool(settings.api_key), "api_key": settings.api_key or None,
+                "key_file": settings.key_file}
+
+    @app.post("/api/admin/api-key/rotate")
+    async def rotate_api_key():
+        """Issue a new random key; the old one stops working with the next
+        request (no restart), and outstanding websocket tickets are dropped."""
+        key = settings.rotate_key()
+        return {"api_key": key, "effective": "now", "key_file": settings.key_file}
+
+    @app.post("/api/admin/ws-ticket")
+    async def ws_ticket():
+        """A one-time, 30-second ticket for /api/admin/ws?t=<ticket>."""
+        return {"ticket": settings.issue_ticket(), "expires_in_s": settings.TICKET_S}
 
     @app.get("/api/admin/storage/breakdown")
     @app.get("/api/admin/storage")

@@ -33,8 +33,8 @@ from __future__ import annotations
 import asyncio
 import dataclasses
 import itertools
-import os
 import json
+import os
 import secrets
 import queue
 import threading
@@ -530,7 +530,10 @@ def _loads_or(v):
 def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "llama",
                chat_template: str | None = None, max_model_len: int = 4096,
                api_key: str | None = None, cors_origins=(), rpm: int = 0, port: int = 8800,
-               store_path: str | None = None, config_path: str | None = None):
+               store_path: str | None = None, config_path: str | None = None,
+               api_key_file: str | None = None):
+    """`api_key_file`: the key is read from it when `api_key` is not given,
+    and a key rotated through the admin API is written back to it."""
     from fastapi import FastAPI
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
@@ -868,7 +871,11 @@ def create_app(aengine: AsyncEngine, tokenizer, model_name: str, arch: str = "ll
             except Exception:
                 pass
 
-    settings = ServerSettings(api_key or None, port, tuple(cors_origins), rpm)
+    if not api_key and api_key_file and os.path.exists(api_key_file):
+        with open(api_key_file) as f:
+            api_key = f.read().strip() or None
+    settings = ServerSettings(api_key or None, port, tuple(cors_origins), rpm,
+                              key_file=api_key_file)
     app.state.settings = settings
     responses.register(app, S, store_path)
     mcp.register(app, S)

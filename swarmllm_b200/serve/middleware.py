@@ -21,9 +21,10 @@ from __future__ import annotations
 
 import hmac
 import json
+import os
 import threading
 import time
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 _EXEMPT = ("/health", "/health/ready")
 _LOOPBACK = ("127.0.0.1", "::1", "localhost")
@@ -88,6 +89,40 @@ class ServerSettings:
     cors_origins: tuple = ()
     rpm: int = 0
     max_body: int = 32 << 20
+    key_file: str | None = None          # where a rotated key is written (0600)
+    ws_tickets: dict = field(default_factory=dict)   # one-time websocket tickets -> expiry
+
+    TICKET_S = 30.0
+
+    def issue_ticket(self, now: float | None = None) -> str:
+        """A one-time ticket for the status websocket (`?t=<ticket>`): a
+        browser cannot set an Authorization header on a websocket, and the
+        key itself should not sit in a URL."""
+        import secrets
+        now = time.monotonic() if now is None else now
+        for t, exp in list(self.ws_tickets.items()):
+            if exp < now:
+                del self.ws_tickets[t]
+        t = secrets.token_hex(16)
+        self.ws_tickets[t] = now + self.TICKET_S
+        return t
+
+    def take_ticket(self, t: str, now: float | None = None) -> bool:
+        exp = self.ws_tickets.pop(t, None)
+        return exp is not None and exp >= (time.monotonic() if now is None else now)
+
+    def rotate_key(self) -> str:
+        """A new random key, in force from the next request; the old one stops
+        working at once (and is overwritten in `key_file` when one is set)."""
+        import secrets
+        key = secrets.token_hex(32)
+        if self.key_file:
+            fd = os.open(self.key_file, os.O_WRONLY | os.O_CREAT | os.O_TRUNC, 0o600)
+            with os.fdopen(fd, "w") as f:
+                f.write(key + "\n")
+        self.api_key = key
+        self.ws_tickets.clear()
+        return key
 
     def public(self) -> dict:
         return {"auth_required": bool(self.api_key), "port": self.port,
@@ -196,7 +231,11 @@ class SecurityMiddleware:
         tok = bearer_or_key(headers)
         if not tok and scope["type"] == "websocket":   # browsers cannot set headers on a websocket
             from urllib.parse import parse_qs
-            tok = (parse_qs(scope.get("query_string", b"").decode()).get("token") or [""])[0]
+            q = parse_qs(scope.get("query_string", b"").decode())
+            ticket = (q.get("t") or [""])[0]
+            if ticket:
+                return self.settings.take_ticket(ticket)
+            tok = (q.get("token") or [""])[0]
         return bool(tok) and key_matches(tok, self.api_key)
 
     @staticmethod

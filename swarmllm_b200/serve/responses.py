@@ -77,6 +77,22 @@ class ResponseStore:
             self.db.commit()
         return n > 0
 
+    def prune(self, older_than_s: float | None = None, keep: int | None = None) -> tuple[int, int]:
+        """Delete stored responses older than `older_than_s` seconds and/or all
+        but the newest `keep`; returns (removed, left)."""
+        with self.lock:
+            n = 0
+            if older_than_s is not None:
+                n += self.db.execute("DELETE FROM responses WHERE created < ?",
+                                     (time.time() - older_than_s,)).rowcount
+            if keep is not None:
+                n += self.db.execute(
+                    "DELETE FROM responses WHERE id NOT IN "
+                    "(SELECT id FROM responses ORDER BY created DESC LIMIT ?)", (max(0, keep),)).rowcount
+            self.db.commit()
+            left = self.db.execute("SELECT COUNT(*) FROM responses").fetchone()[0]
+        return n, left
+
 
 class _Run:
     """A background run: its task, its event log and waiters."""

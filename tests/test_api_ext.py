@@ -587,3 +587,50 @@ def test_unseeded_requests_draw_fresh_seeds():
         assert seen[-1].seed == 7
         assert c.post("/v1/chat/completions", json={"messages": msgs, "seed": "x"}).status_code == 400
     ae.shutdown()
+
+
+def test_api_key_rotation_and_ws_tickets(tmp_path):
+    """Rotation takes effect with the next request and is written to the key
+    file; a websocket ticket works once and the key never goes in the URL."""
+    kf = tmp_path / "key"
+    kf.write_text("k0\n")
+    c, ae, _ = _client("ok", api_key_file=str(kf))
+    H0 = {"Authorization": "Bearer k0"}
+    with c:
+        assert c.get("/api/admin/api-key").status_code == 401
+        assert c.get("/api/admin/api-key", headers=H0).json()["api_key"] == "k0"
+        new = c.post("/api/admin/api-key/rotate", headers=H0).json()["api_key"]
+        assert len(new) == 64 and new != "k0"
+        assert kf.read_text().strip() == new
+        assert c.get("/v1/models", headers=H0).status_code == 401          # old key: out
+        H1 = {"Authorization": f"Bearer {new}"}
+        assert c.get("/v1/models", headers=H1).status_code == 200
+        t = c.post("/api/admin/ws-ticket", headers=H1).json()["ticket"]
+        with c.websocket_connect(f"/api/admin/ws?n=1&t={t}") as ws:
+            assert ws.receive_json()["type"] == "status"
+        import pytest as _pt
+        from starlette.websockets import WebSocketDisconnect
+        with _pt.raises(WebSocketDisconnect):                              # a ticket is single-use
+            with c.websocket_connect(f"/api/admin/ws?n=1&t={t}") as ws:
+                ws.receive_json()
+    ae.shutdown()
+
+
+def test_prune_history(tmp_path):
+    import time as _t
+    c, ae, _ = _client("ok")
+    with c:
+        store = c.app.state.response_store
+        for i in range(5):
+            store.put({"id": f"resp_{i}"}, [], [])
+        with store.lock:   # age two of them by three days
+            store.db.execute("UPDATE responses SET created = ? WHERE id IN ('resp_0', 'resp_1')",
+                             (_t.time() - 3 * 86400,))
+            store.db.commit()
+        r = c.post("/api/admin/prune-history", json={"older_than_days": 2}).json()
+        assert r == {"removed": 2, "left": 3}
+        r = c.post("/api/admin/prune-history", json={"keep": 1}).json()
+        assert r == {"removed": 2, "left": 1}
+        assert c.post("/api/admin/prune-history", json={}).status_code == 400
+        assert c.post("/api/admin/prune-history", json={"keep": -1}).status_code == 400
+    ae.shutdown()
