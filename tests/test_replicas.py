@@ -154,3 +154,47 @@ def test_http_server_over_replicas():
         th.join(5)
         ae.shutdown()
         rs.close()
+
+
+def _flaky_factory(spec, idx):
+    """Replica 1's engine fails on its third step (a stand-in for a device
+    error); replica 0 is healthy."""
+    from swarmllm_b200.parallel.replicas import engine_factory
+    eng = engine_factory(spec, idx)
+    if idx == 1:
+        real, n = eng.step, [0]
+
+        def step():
+            n[0] += 1
+            if n[0] >= 3:
+                raise RuntimeError("device lost")
+            return real()
+        eng.step = step
+    return eng
+
+
+def test_a_replica_failing_mid_run_fails_only_its_requests():
+    from swarmllm_b200.engine import SamplingParams
+    from swarmllm_b200.parallel.replicas import ReplicaSet
+    cfg, spec = _spec()
+    rs = ReplicaSet(cfg, spec, 2, factory=_flaky_factory)
+    try:
+        sp = SamplingParams(max_tokens=6, ignore_eos=True)
+        rids = [rs.add_request([1, 2, 3 + i], sp) for i in range(4)]
+        on = {rid: rs.reqs[rid].replica for rid in rids}
+        assert set(on.values()) == {0, 1}
+        done = {}
+        while rs.has_work():
+            for rid, tok, fin in rs.step(0.1):
+                if fin:
+                    done[rid] = tok
+        for rid in rids:
+            if on[rid] == 1:
+                assert done[rid] is None and "device lost" in rs.error_of(rid)
+            else:
+                assert rs.error_of(rid) is None and len(rs.output(rid)) == 6
+        assert 1 in rs.dead
+        late = rs.generate([[9, 9, 9]], sp)          # new work goes to the survivor
+        assert late[0].replica == 0 and len(late[0].token_ids) == 6
+    finally:
+        rs.close()
