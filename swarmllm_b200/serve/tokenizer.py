@@ -15,6 +15,11 @@ from __future__ import annotations
 
 import re
 
+try:   # \p{L} / \p{N} classes for the pre-tokenizer patterns
+    import regex as _rx
+except ImportError:  # pragma: no cover -- the stdlib fallback keeps one pattern
+    _rx = None
+
 
 def _bytes_to_unicode() -> dict[int, str]:
     """The reversible byte -> printable-unicode map of byte-level BPE
@@ -48,13 +53,75 @@ class ByteTokenizer:
         return self.decode([i])
 
 
+# Pre-tokenizer patterns (the public definitions of each tokenizer family: a
+# BPE vocabulary only reproduces its training splits with the same pattern).
+_APOS = r"(?:'[sS]|'[tT]|'[rR][eE]|'[vV][eE]|'[mM]|'[lL][lL]|'[dD])"
+_PAT_GPT2 = r"'s|'t|'re|'ve|'m|'ll|'d| ?\p{L}+| ?\p{N}+| ?[^\s\p{L}\p{N}]+|\s+(?!\S)|\s+"
+_PAT_LLAMA3 = (_APOS + r"|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}{1,3}| ?[^\s\p{L}\p{N}]+[\r\n]*"
+               r"|\s*[\r\n]+|\s+(?!\S)|\s+")
+_PAT_QWEN2 = (_APOS + r"|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}| ?[^\s\p{L}\p{N}]+[\r\n]*"
+              r"|\s*[\r\n]+|\s+(?!\S)|\s+")
+# Qwen 3.5: combining marks stay with their letters
+_PAT_QWEN35 = (_APOS + r"|[^\r\n\p{L}\p{N}]?[\p{L}\p{M}]+|\p{N}| ?[^\s\p{L}\p{M}\p{N}]+[\r\n]*"
+               r"|\s*[\r\n]+|\s+(?!\S)|\s+")
+_UP, _LO = r"[\p{Lu}\p{Lt}\p{Lm}\p{Lo}\p{M}]", r"[\p{Ll}\p{Lm}\p{Lo}\p{M}]"
+# GPT-4o / o200k (gpt-oss, Llama 4): case runs split, digits in threes
+_PAT_GPT4O = (r"[^\r\n\p{L}\p{N}]?" + _UP + "*" + _LO + "+" + _APOS + "?"
+              r"|[^\r\n\p{L}\p{N}]?" + _UP + "+" + _LO + "*" + _APOS + "?"
+              r"|\p{N}{1,3}| ?[^\s\p{L}\p{N}]+[\r\n/]*|\s*[\r\n]+|\s+(?!\S)|\s+")
+# Mistral tekken: as GPT-4o without the contractions, single digits
+_PAT_TEKKEN = (r"[^\r\n\p{L}\p{N}]?" + _UP + "*" + _LO + "+"
+               r"|[^\r\n\p{L}\p{N}]?" + _UP + "+" + _LO + "*"
+               r"|\p{N}| ?[^\s\p{L}\p{N}]+[\r\n/]*|\s*[\r\n]+|\s+(?!\S)|\s+")
+
+# tokenizer.ggml.pre -> patterns applied in sequence (each re-splits the
+# previous pass's pieces)
+PRE_TOKENIZERS = {
+    **{k: (_PAT_LLAMA3,) for k in ("llama3", "llama-v3", "llama-bpe", "smaug-bpe", "dbrx",
+                                   "falcon3", "pixtral", "glm4", "chatglm-bpe")},
+    **{k: (_PAT_QWEN2,) for k in ("qwen2", "deepseek-r1-qwen", "stablelm2", "megrez", "hunyuan")},
+    "qwen35": (_PAT_QWEN35,),
+    **{k: (_PAT_GPT4O,) for k in ("gpt-4o", "llama4", "minimax-m2")},
+    "tekken": (_PAT_TEKKEN,),
+    **{k: (_PAT_GPT2,) for k in ("gpt-2", "gpt2", "phi-2", "olmo", "mpt", "roberta-bpe")},
+    "default": (r"[\p{P}\$\+<=>\^~\|]+", _PAT_GPT2, r"\p{N}+", r"[0-9][0-9][0-9]"),
+    **{k: (r"\p{N}", _PAT_GPT2) for k in ("starcoder", "refact", "command-r", "smollm")},
+    "whitespace": (r"\S+|\s+",),
+}
+
+
+def pre_split(text: str, patterns) -> list[str]:
+    """Split `text` by each compiled pattern in turn; the text between
+    matches stays as its own piece, so nothing is dropped."""
+    pieces = [text]
+    for pat in patterns:
+        out = []
+        for piece in pieces:
+            pos = 0
+            for m in pat.finditer(piece):
+                if m.start() > pos:
+                    out.append(piece[pos:m.start()])
+                if m.end() > m.start():
+                    out.append(m.group())
+                pos = m.end()
+            if pos < len(piece):
+                out.append(piece[pos:])
+        pieces = out
+    return pieces
+
+
 class BPETokenizer:
-    # Llama-3 / GPT-4-style pre-tokenizer split (letters, numbers, punctuation, spaces)
+    # fallback pre-tokenizer (Llama 3 style) when the regex module is missing
     PAT = re.compile(r"""'(?:[sdmt]|ll|ve|re)| ?[^\W\d_]+| ?\d{1,3}| ?[^\s\w]+[\r\n]*|\s*[\r\n]+|\s+(?!\S)|\s+""",
                      re.UNICODE)
 
     def __init__(self, tokens: list[str], merges: list[str], bos_id: int = -1, eos_id: int = -1,
-                 token_types: list[int] | None = None):
+                 token_types: list[int] | None = None, pre: str | None = None):
+        """`pre`: the GGUF `tokenizer.ggml.pre` name (Llama 3's pattern when
+        absent or unknown)."""
+        self.pre = pre if pre in PRE_TOKENIZERS else "llama3"
+        self.patterns = (tuple(_rx.compile(p) for p in PRE_TOKENIZERS[self.pre])
+                         if _rx is not None else (self.PAT,))
         self.tokens = tokens
         self.vocab = {t: i for i, t in enumerate(tokens)}
         self.ranks = {}
@@ -105,7 +172,7 @@ class BPETokenizer:
             if ch in self.special:
                 ids.append(self.special[ch])
                 continue
-            for w in self.PAT.findall(ch):
+            for w in pre_split(ch, self.patterns):
                 ids.extend(self._bpe("".join(self.b2u[b] for b in w.encode("utf-8"))))
         return ids
 
@@ -190,7 +257,7 @@ def from_gguf_metadata(md: dict, vocab_size: int):
     eos = int(md.get("tokenizer.ggml.eos_token_id", -1))
     if toks and model == "gpt2":
         return BPETokenizer(toks, md.get("tokenizer.ggml.merges", []), bos, eos,
-                            md.get("tokenizer.ggml.token_type"))
+                            md.get("tokenizer.ggml.token_type"), md.get("tokenizer.ggml.pre"))
     if toks and model == "llama":
         return SPMTokenizer(toks, md.get("tokenizer.ggml.scores", [0.0] * len(toks)), bos, eos)
     return ByteTokenizer(vocab_size)
