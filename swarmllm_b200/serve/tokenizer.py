@@ -199,7 +199,15 @@ class BPETokenizer:
 
 
 class SPMTokenizer:
-    def __init__(self, tokens: list[str], scores: list[float], bos_id: int = 1, eos_id: int = 2):
+    """SentencePiece-style BPE over the whole text (a dummy-prefix '▁', spaces
+    as '▁'): the highest-scoring adjacent pair that is a vocabulary entry merges
+    first, leftmost among equals, with a heap of candidate pairs over a linked
+    list of symbols (O(n log n)); pieces outside the vocabulary fall back to
+    byte tokens <0xNN>.  Control and user-defined tokens (token types 3 / 4)
+    in the text are matched whole first, as the BPE tokenizer does."""
+
+    def __init__(self, tokens: list[str], scores: list[float], bos_id: int = 1, eos_id: int = 2,
+                 token_types: list[int] | None = None):
         self.tokens, self.scores = tokens, scores
         self.vocab = {t: i for i, t in enumerate(tokens)}
         self.bos_id, self.eos_id = bos_id, eos_id
@@ -208,27 +216,71 @@ class SPMTokenizer:
             m = re.fullmatch(r"<0x([0-9A-Fa-f]{2})>", t)
             if m:
                 self.byte_ids[int(m.group(1), 16)] = i
+        self.special = {t: i for i, t in enumerate(tokens)
+                        if token_types and i < len(token_types) and token_types[i] in (3, 4)
+                        and i not in (bos_id, eos_id) and t}
         self.vocab_size = len(tokens)
 
-    def encode(self, text: str, add_bos: bool = True) -> list[int]:
-        text = "▁" + text.replace(" ", "▁")
-        parts = list(text)
-        while True:
-            best, bi = None, -1
-            for i in range(len(parts) - 1):
-                cand = parts[i] + parts[i + 1]
-                j = self.vocab.get(cand)
-                if j is not None and (best is None or self.scores[j] > best):
-                    best, bi = self.scores[j], i
-            if best is None:
-                break
-            parts[bi:bi + 2] = [parts[bi] + parts[bi + 1]]
-        ids = [self.bos_id] if add_bos else []
-        for p in parts:
+    def _merge(self, text: str) -> list[int]:
+        import heapq
+        sym = list(text)
+        n = len(sym)
+        nxt = list(range(1, n + 1))
+        prv = list(range(-1, n - 1))
+        alive = [True] * n
+        heap = []
+
+        def push(i):
+            j = nxt[i]
+            if j < n:
+                k = self.vocab.get(sym[i] + sym[j])
+                if k is not None:
+                    heapq.heappush(heap, (-self.scores[k], i, sym[i], sym[j]))
+        for i in range(n - 1):
+            push(i)
+        while heap:
+            _, i, a, b = heapq.heappop(heap)
+            j = nxt[i] if i < n else n
+            # stale: a side merged since this pair was pushed
+            if not alive[i] or j >= n or sym[i] != a or sym[j] != b:
+                continue
+            sym[i] = a + b
+            alive[j] = False
+            nxt[i] = nxt[j]
+            if nxt[j] < n:
+                prv[nxt[j]] = i
+            if prv[i] >= 0:
+                push(prv[i])
+            push(i)
+        ids = []
+        i = 0
+        while i < n:
+            p = sym[i]
             if p in self.vocab:
                 ids.append(self.vocab[p])
             else:
                 ids.extend(self.byte_ids.get(b, 0) for b in p.encode("utf-8"))
+            i = nxt[i]
+        return ids
+
+    def encode(self, text: str, add_bos: bool = True) -> list[int]:
+        ids = [self.bos_id] if add_bos and self.bos_id >= 0 else []
+        if self.special:
+            pat = "(" + "|".join(re.escape(t) for t in sorted(self.special, key=len, reverse=True)) + ")"
+            chunks = re.split(pat, text)
+        else:
+            chunks = [text]
+        first = True
+        for ch in chunks:
+            if not ch:
+                continue
+            if ch in self.special:
+                ids.append(self.special[ch])
+                first = False
+                continue
+            # the dummy prefix goes before the text's first piece only
+            ids.extend(self._merge(("▁" if first else "") + ch.replace(" ", "▁")))
+            first = False
         return ids
 
     def decode(self, ids) -> str:
@@ -259,5 +311,6 @@ def from_gguf_metadata(md: dict, vocab_size: int):
         return BPETokenizer(toks, md.get("tokenizer.ggml.merges", []), bos, eos,
                             md.get("tokenizer.ggml.token_type"), md.get("tokenizer.ggml.pre"))
     if toks and model == "llama":
-        return SPMTokenizer(toks, md.get("tokenizer.ggml.scores", [0.0] * len(toks)), bos, eos)
+        return SPMTokenizer(toks, md.get("tokenizer.ggml.scores", [0.0] * len(toks)), bos, eos,
+                            md.get("tokenizer.ggml.token_type"))
     return ByteTokenizer(vocab_size)

@@ -32,3 +32,54 @@ def test_bpe_tokenizer_uses_the_gguf_pre_name():
     assert ll.encode("12", add_bos=False) == [256]         # one piece "12": merged
     assert q.decode(q.encode("a 12 b", add_bos=False)) == "a 12 b"
     assert BPETokenizer(toks, merges, pre="no-such-pre").pre == "llama3"
+
+
+def _naive_spm(tok, text):
+    """The definition: repeatedly merge the best-scoring adjacent pair
+    (leftmost among equals) over the whole text; empty text has no pieces."""
+    if not text:
+        return []
+    parts = list("▁" + text.replace(" ", "▁"))
+    while True:
+        best, bi = None, -1
+        for i in range(len(parts) - 1):
+            j = tok.vocab.get(parts[i] + parts[i + 1])
+            if j is not None and (best is None or tok.scores[j] > best):
+                best, bi = tok.scores[j], i
+        if best is None:
+            break
+        parts[bi:bi + 2] = [parts[bi] + parts[bi + 1]]
+    out = []
+    for p in parts:
+        out += [tok.vocab[p]] if p in tok.vocab else [tok.byte_ids.get(b, 0) for b in p.encode()]
+    return out
+
+
+def test_spm_heap_merge_matches_the_definition():
+    import random
+
+    from swarmllm_b200.serve.tokenizer import SPMTokenizer
+    rng = random.Random(0)
+    alpha = "ab c▁"
+    pieces = set("abc▁")
+    while len(pieces) < 60:
+        pieces.add("".join(rng.choice("abc▁") for _ in range(rng.randint(2, 4))))
+    toks = ["<unk>", "<s>", "</s>"] + [f"<0x{b:02X}>" for b in range(256)] + sorted(pieces)
+    scores = [0.0] * 259 + [float(rng.randint(-5, 5)) for _ in sorted(pieces)]   # many ties
+    tok = SPMTokenizer(toks, scores, 1, 2)
+    for _ in range(300):
+        text = "".join(rng.choice(alpha) for _ in range(rng.randint(0, 30)))
+        assert tok.encode(text, add_bos=False) == _naive_spm(tok, text), text
+    assert tok.decode(tok.encode("ab c", add_bos=True)) == "ab c"
+
+
+def test_spm_special_tokens_stay_whole():
+    from swarmllm_b200.serve.tokenizer import SPMTokenizer
+    toks = (["<unk>", "<s>", "</s>", "<start_of_turn>"] + [f"<0x{b:02X}>" for b in range(256)]
+            + ["▁", "h", "i", "▁h", "hi", "▁hi"])
+    types = [2, 3, 3, 3] + [6] * 256 + [1] * 6
+    scores = [0.0] * 260 + [0.0, 0.0, 0.0, 1.0, 2.0, 3.0]
+    tok = SPMTokenizer(toks, scores, 1, 2, types)
+    ids = tok.encode("<start_of_turn>hi", add_bos=False)
+    assert ids[0] == 3 and ids[1:] == [tok.vocab["hi"]]
+    assert tok.encode("hi", add_bos=False) == [tok.vocab["▁hi"]]
