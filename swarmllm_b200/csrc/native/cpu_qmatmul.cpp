@@ -101,85 +101,6 @@ struct Acts {
   int K;
 };
 
-// One Q4_K block (256 values, 144 bytes) against tokens t0..t0+nt.
-void block_q4k(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
-  const float d = half_to_float(rd16(blk)), dmin = half_to_float(rd16(blk + 2));
-  const uint8_t* sc = blk + 4;
-  const uint8_t* qs = blk + 16;
-  alignas(64) int8_t q[256];
-  for (int g = 0; g < 4; ++g)
-    for (int l = 0; l < 32; ++l) {
-      q[64 * g + l] = (int8_t)(qs[32 * g + l] & 0xF);
-      q[64 * g + 32 + l] = (int8_t)(qs[32 * g + l] >> 4);
-    }
-  float ds[8], dm[8];
-  for (int j = 0; j < 8; ++j) {
-    int s, m;
-    if (j < 4) {
-      s = sc[j] & 63;
-      m = sc[j + 4] & 63;
-    } else {
-      s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
-      m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-    }
-    ds[j] = d * (float)s;
-    dm[j] = dmin * (float)m;
-  }
-  const int nb = a.K / 32;
-  for (int t = 0; t < nt; ++t) {
-    const int8_t* xq = a.q + (size_t)(t0 + t) * a.K + 256 * b;
-    const float* dx = a.dx + (size_t)(t0 + t) * nb + 8 * b;
-    const int32_t* sx = a.sx + (size_t)(t0 + t) * nb + 8 * b;
-    float v = 0.f;
-    for (int j = 0; j < 8; ++j)
-      v += dx[j] * (ds[j] * (float)dot_i8(q + 32 * j, xq + 32 * j, 32) - dm[j] * (float)sx[j]);
-    acc[t] += v;
-  }
-}
-
-// One Q6_K block (256 values, 210 bytes).
-void block_q6k(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
-  const uint8_t* ql = blk;
-  const uint8_t* qh = blk + 128;
-  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
-  const float d = half_to_float(rd16(blk + 208));
-  alignas(64) int8_t q[256];
-  for (int n = 0; n < 2; ++n)
-    for (int l = 0; l < 32; ++l) {
-      const int h = qh[32 * n + l];
-      const int l0 = ql[64 * n + l], l1 = ql[64 * n + 32 + l];
-      q[128 * n + l] = (int8_t)(((l0 & 0xF) | ((h & 3) << 4)) - 32);
-      q[128 * n + 32 + l] = (int8_t)(((l1 & 0xF) | (((h >> 2) & 3) << 4)) - 32);
-      q[128 * n + 64 + l] = (int8_t)(((l0 >> 4) | (((h >> 4) & 3) << 4)) - 32);
-      q[128 * n + 96 + l] = (int8_t)(((l1 >> 4) | (((h >> 6) & 3) << 4)) - 32);
-    }
-  float ds[16];
-  for (int s = 0; s < 16; ++s) ds[s] = d * (float)sc[s];
-  const int nb = a.K / 32;
-  for (int t = 0; t < nt; ++t) {
-    const int8_t* xq = a.q + (size_t)(t0 + t) * a.K + 256 * b;
-    const float* dx = a.dx + (size_t)(t0 + t) * nb + 8 * b;
-    float v = 0.f;
-    for (int s = 0; s < 16; ++s) v += ds[s] * dx[s >> 1] * (float)dot_i8(q + 16 * s, xq + 16 * s, 16);
-    acc[t] += v;
-  }
-}
-
-// One Q4_0 block (32 values, 18 bytes: d, then value j's code in the low
-// nibble of byte j and value j + 16's in its high nibble; x = d (q - 8)).
-void block_q40(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
-  const float d = half_to_float(rd16(blk));
-  int8_t q[32];
-  for (int j = 0; j < 16; ++j) {
-    q[j] = (int8_t)((blk[2 + j] & 0xF) - 8);
-    q[16 + j] = (int8_t)((blk[2 + j] >> 4) - 8);
-  }
-  const int nb = a.K / 32;
-  for (int t = 0; t < nt; ++t)
-    acc[t] += d * a.dx[(size_t)(t0 + t) * nb + b] *
-              (float)dot_i8(q, a.q + (size_t)(t0 + t) * a.K + 32 * b, 32);
-}
-
 // The 4-bit code books of the table formats (value = scale * code).
 constexpr int8_t kIq4Code[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
                                  1,    13,   25,  38,  53,  69,  89,  113};
@@ -190,24 +111,6 @@ constexpr int8_t kMxfp4Code[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -
 // Block scale of a table format: fp16 d (IQ4_NL) or E8M0 exponent (MXFP4).
 inline float lut_scale(int type, const uint8_t* blk) {
   return type == kGgmlIQ4_NL ? half_to_float(rd16(blk)) : std::ldexp(1.f, (int)blk[0] - 128);
-}
-
-// One IQ4_NL (18 bytes) or MXFP4 (17 bytes) block of 32 values: codes in the
-// nibbles as Q4_0 keeps them, mapped through the format's code book.
-template <int TYPE>
-void block_lut4(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
-  constexpr int HDR = TYPE == kGgmlIQ4_NL ? 2 : 1;
-  const int8_t* book = TYPE == kGgmlIQ4_NL ? kIq4Code : kMxfp4Code;
-  const float d = lut_scale(TYPE, blk);
-  int8_t q[32];
-  for (int j = 0; j < 16; ++j) {
-    q[j] = book[blk[HDR + j] & 0xF];
-    q[16 + j] = book[blk[HDR + j] >> 4];
-  }
-  const int nb = a.K / 32;
-  for (int t = 0; t < nt; ++t)
-    acc[t] += d * a.dx[(size_t)(t0 + t) * nb + b] *
-              (float)dot_i8(q, a.q + (size_t)(t0 + t) * a.K + 32 * b, 32);
 }
 
 // IQ4_XS sub-block scales: d * (ls_j - 32), ls_j six bits (4 low in
@@ -221,36 +124,124 @@ inline void iq4xs_scales(const uint8_t* blk, float* dl) {
   }
 }
 
-// One IQ4_XS block (256 values, 136 bytes: d, scales_h, scales_l[4], qs[128];
-// sub-block j's codes in qs[16j..] as Q4_0 keeps a block's).
-void block_iq4xs(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
-  float dl[8];
-  iq4xs_scales(blk, dl);
+// One block decoded to integer codes and per-sub-block affine maps:
+// value[i] = scale[i / sub] * q[i] + offset[i / sub].
+struct Decoded {
   int8_t q[256];
-  for (int j = 0; j < 8; ++j)
-    for (int i = 0; i < 16; ++i) {
-      const uint8_t c = blk[8 + 16 * j + i];
-      q[32 * j + i] = kIq4Code[c & 0xF];
-      q[32 * j + 16 + i] = kIq4Code[c >> 4];
+  float scale[16], offset[16];
+  int n, sub;  // values in the block, values per sub-block
+};
+
+void decode_block(int type, const uint8_t* blk, Decoded& o) {
+  switch (type) {
+    case kGgmlQ4_K: {
+      const float d = half_to_float(rd16(blk)), dmin = half_to_float(rd16(blk + 2));
+      const uint8_t* sc = blk + 4;
+      const uint8_t* qs = blk + 16;
+      for (int g = 0; g < 4; ++g)
+        for (int l = 0; l < 32; ++l) {
+          o.q[64 * g + l] = (int8_t)(qs[32 * g + l] & 0xF);
+          o.q[64 * g + 32 + l] = (int8_t)(qs[32 * g + l] >> 4);
+        }
+      for (int j = 0; j < 8; ++j) {
+        int sv, m;
+        if (j < 4) {
+          sv = sc[j] & 63;
+          m = sc[j + 4] & 63;
+        } else {
+          sv = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+          m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+        }
+        o.scale[j] = d * (float)sv;
+        o.offset[j] = -dmin * (float)m;
+      }
+      o.n = 256;
+      o.sub = 32;
+      return;
     }
-  const int nb = a.K / 32;
-  for (int t = 0; t < nt; ++t) {
-    const int8_t* xq = a.q + (size_t)(t0 + t) * a.K + 256 * b;
-    const float* dx = a.dx + (size_t)(t0 + t) * nb + 8 * b;
-    float v = 0.f;
-    for (int j = 0; j < 8; ++j) v += dl[j] * dx[j] * (float)dot_i8(q + 32 * j, xq + 32 * j, 32);
-    acc[t] += v;
+    case kGgmlQ6_K: {
+      const uint8_t* ql = blk;
+      const uint8_t* qh = blk + 128;
+      const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192);
+      const float d = half_to_float(rd16(blk + 208));
+      for (int n = 0; n < 2; ++n)
+        for (int l = 0; l < 32; ++l) {
+          const int h = qh[32 * n + l];
+          const int l0 = ql[64 * n + l], l1 = ql[64 * n + 32 + l];
+          o.q[128 * n + l] = (int8_t)(((l0 & 0xF) | ((h & 3) << 4)) - 32);
+          o.q[128 * n + 32 + l] = (int8_t)(((l1 & 0xF) | (((h >> 2) & 3) << 4)) - 32);
+          o.q[128 * n + 64 + l] = (int8_t)(((l0 >> 4) | (((h >> 4) & 3) << 4)) - 32);
+          o.q[128 * n + 96 + l] = (int8_t)(((l1 >> 4) | (((h >> 6) & 3) << 4)) - 32);
+        }
+      for (int j = 0; j < 16; ++j) {
+        o.scale[j] = d * (float)sc[j];
+        o.offset[j] = 0.f;
+      }
+      o.n = 256;
+      o.sub = 16;
+      return;
+    }
+    case kGgmlIQ4_XS: {
+      iq4xs_scales(blk, o.scale);
+      for (int j = 0; j < 8; ++j) {
+        o.offset[j] = 0.f;
+        for (int i = 0; i < 16; ++i) {
+          const uint8_t c = blk[8 + 16 * j + i];
+          o.q[32 * j + i] = kIq4Code[c & 0xF];
+          o.q[32 * j + 16 + i] = kIq4Code[c >> 4];
+        }
+      }
+      o.n = 256;
+      o.sub = 32;
+      return;
+    }
+    case kGgmlQ8_0: {
+      o.scale[0] = half_to_float(rd16(blk));
+      std::memcpy(o.q, blk + 2, 32);
+      break;
+    }
+    default: {  // Q4_0, IQ4_NL, MXFP4: 32 codes in the nibbles of 16 bytes
+      const int hdr = type == kGgmlMXFP4 ? 1 : 2;
+      o.scale[0] = type == kGgmlQ4_0 ? half_to_float(rd16(blk)) : lut_scale(type, blk);
+      for (int j = 0; j < 16; ++j) {
+        const uint8_t c = blk[hdr + j];
+        if (type == kGgmlQ4_0) {
+          o.q[j] = (int8_t)((c & 0xF) - 8);
+          o.q[16 + j] = (int8_t)((c >> 4) - 8);
+        } else {
+          const int8_t* book = type == kGgmlIQ4_NL ? kIq4Code : kMxfp4Code;
+          o.q[j] = book[c & 0xF];
+          o.q[16 + j] = book[c >> 4];
+        }
+      }
+      break;
+    }
   }
+  o.offset[0] = 0.f;
+  o.n = 32;
+  o.sub = 32;
 }
 
-// One Q8_0 block (32 values, 34 bytes).
-void block_q80(const uint8_t* blk, int b, const Acts& a, int t0, int nt, float* acc) {
-  const float d = half_to_float(rd16(blk));
-  const int8_t* q = reinterpret_cast<const int8_t*>(blk + 2);
-  const int nb = a.K / 32;
-  for (int t = 0; t < nt; ++t)
-    acc[t] += d * a.dx[(size_t)(t0 + t) * nb + b] *
-              (float)dot_i8(q, a.q + (size_t)(t0 + t) * a.K + 32 * b, 32);
+// One block of any format against tokens t0..t0+nt (the portable path).
+// A sub-block's activation scale is the one of its 32-value activation
+// block; an offset (Q4_K's -dmin m) meets the sum of the rounded activations.
+void block_generic(int type, const uint8_t* blk, int vpos, const Acts& a, int t0, int nt,
+                   float* acc) {
+  Decoded o;
+  decode_block(type, blk, o);
+  const int nb = a.K / 32, ns = o.n / o.sub;
+  for (int t = 0; t < nt; ++t) {
+    const int8_t* xq = a.q + (size_t)(t0 + t) * a.K + vpos;
+    const float* dx = a.dx + (size_t)(t0 + t) * nb + vpos / 32;
+    const int32_t* sx = a.sx + (size_t)(t0 + t) * nb + vpos / 32;
+    float v = 0.f;
+    for (int j = 0; j < ns; ++j) {
+      const int x32 = j * o.sub / 32;
+      v += o.scale[j] * dx[x32] * (float)dot_i8(o.q + j * o.sub, xq + j * o.sub, o.sub);
+      if (o.offset[j] != 0.f) v += o.offset[j] * dx[x32] * (float)sx[x32];
+    }
+    acc[t] += v;
+  }
 }
 
 size_t row_bytes_of(int type, int K) {
@@ -555,28 +546,38 @@ int cpu_qmatmul(const uint8_t* w, int type, int rows, int K, const float* x, int
     return 0;
   }
   const size_t row_bytes = row_bytes_of(type, K);
-  const int nblk = small_blocks ? K / 32 : K / 256;
-  const size_t blk_bytes = type == kGgmlQ4_K   ? 144
-                           : type == kGgmlQ6_K ? 210
-                           : type == kGgmlQ8_0 ? 34
-                           : type == kGgmlMXFP4 ? 17
-                           : type == kGgmlIQ4_XS ? 136
-                                               : 18;
-  auto* fn = type == kGgmlQ4_K     ? block_q4k
-             : type == kGgmlQ6_K   ? block_q6k
-             : type == kGgmlQ8_0   ? block_q80
-             : type == kGgmlQ4_0   ? block_q40
-             : type == kGgmlIQ4_NL ? block_lut4<kGgmlIQ4_NL>
-             : type == kGgmlMXFP4  ? block_lut4<kGgmlMXFP4>
-                                   : block_iq4xs;
+  const int bvals = small_blocks ? 32 : 256;
+  const int nblk = K / bvals;
+  const size_t blk_bytes = row_bytes / nblk;
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < rows; ++r) {
     const uint8_t* wr = w + (size_t)r * row_bytes;
     for (int t0 = 0; t0 < T; t0 += kTT) {
       const int nt = T - t0 < kTT ? T - t0 : kTT;
       float acc[kTT] = {};
-      for (int b = 0; b < nblk; ++b) fn(wr + (size_t)b * blk_bytes, b, acts, t0, nt, acc);
+      for (int b = 0; b < nblk; ++b)
+        block_generic(type, wr + (size_t)b * blk_bytes, b * bvals, acts, t0, nt, acc);
       for (int t = 0; t < nt; ++t) out[(size_t)(t0 + t) * rows + r] = acc[t];
+    }
+  }
+  return 0;
+}
+
+int cpu_dequant(const uint8_t* w, int type, int rows, int K, float* out) {
+  const bool small_blocks = type == kGgmlQ8_0 || type == kGgmlQ4_0 || type == kGgmlIQ4_NL ||
+                            type == kGgmlMXFP4;
+  if (K % (small_blocks ? 32 : 256) != 0) return -1;
+  if (type != kGgmlQ4_K && type != kGgmlQ6_K && type != kGgmlIQ4_XS && !small_blocks) return -2;
+  const size_t row_bytes = row_bytes_of(type, K);
+  const int bvals = small_blocks ? 32 : 256, nblk = K / bvals;
+  const size_t blk_bytes = row_bytes / nblk;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < rows; ++r) {
+    Decoded o;
+    for (int b = 0; b < nblk; ++b) {
+      decode_block(type, w + (size_t)r * row_bytes + (size_t)b * blk_bytes, o);
+      float* dst = out + (size_t)r * K + (size_t)b * bvals;
+      for (int i = 0; i < o.n; ++i) dst[i] = o.scale[i / o.sub] * (float)o.q[i] + o.offset[i / o.sub];
     }
   }
   return 0;

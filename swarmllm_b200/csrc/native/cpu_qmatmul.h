@@ -18,6 +18,9 @@ constexpr int kGgmlMXFP4 = 39;
 // Returns 0, or < 0 for an unsupported type or K.
 int cpu_qmatmul(const uint8_t* w, int type, int rows, int K, const float* x, int T, float* out);
 
+// out [rows, K] fp32 = the weight's values (the blocks' scales applied).
+int cpu_dequant(const uint8_t* w, int type, int rows, int K, float* out);
+
 // "avx512vnni" or "generic": the path cpu_qmatmul takes on this CPU
 // (SWARMLLM_CPU_ISA=generic forces the portable one).
 const char* cpu_qmatmul_isa();

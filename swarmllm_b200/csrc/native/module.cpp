@@ -114,6 +114,22 @@ PYBIND11_MODULE(_native, m) {
       py::arg("w"), py::arg("type"), py::arg("rows"), py::arg("K"), py::arg("x"),
       "x [T, K] fp32 times the GGUF-quantized W [rows, K]^T, int8 activations, OpenMP rows");
   m.def("cpu_qmatmul_isa", [] { return std::string(cpu_qmatmul_isa()); });
+  m.def(
+      "cpu_dequant",
+      [](py::array_t<uint8_t, py::array::c_style> w, int type, int rows, int K) {
+        py::array_t<float> out({(py::ssize_t)rows, (py::ssize_t)K});
+        const uint8_t* wp = w.data();
+        float* op = out.mutable_data();
+        int rc;
+        {
+          py::gil_scoped_release nogil;
+          rc = cpu_dequant(wp, type, rows, K, op);
+        }
+        if (rc != 0) throw std::invalid_argument("cpu_dequant: unsupported type or K");
+        return out;
+      },
+      py::arg("w"), py::arg("type"), py::arg("rows"), py::arg("K"),
+      "the fp32 values of `rows` rows of GGUF blocks");
 
   using f32a = py::array_t<float, py::array::c_style | py::array::forcecast>;
   using i32a = py::array_t<int32_t, py::array::c_style | py::array::forcecast>;

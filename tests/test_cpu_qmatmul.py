@@ -97,3 +97,29 @@ def test_cpu_qmatmul_small_blocks_any_width(qtype):
     out = _native.cpu_qmatmul(w, qtype, rows, K, x)
     ref = _round_like_kernel(x) @ wf.T
     assert np.abs(out - ref).max() <= 2e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("qtype", [Q.Q4_K, Q.Q6_K, Q.Q8_0, Q.Q4_0, Q.IQ4_NL, Q.IQ4_XS, Q.MXFP4])
+def test_cpu_dequant_matches_the_format(qtype):
+    rng = np.random.default_rng(qtype)
+    rows, K = 12, 512
+    w = Q.random_quantized(rows, K, qtype, rng=rng)
+    got = _native.cpu_dequant(w, qtype, rows, K)
+    want = Q.dequantize(w, qtype, rows * K).reshape(rows, K)
+    assert np.allclose(got, want, rtol=1e-6, atol=1e-7)
+
+
+def test_prefill_rows_take_the_dequantized_gemm(monkeypatch):
+    """From PREFILL_T rows on, _QWeight multiplies the dequantized slabs in
+    fp32 (exact activations): equal to the fp32 product."""
+    import torch
+
+    from swarmllm_b200.models.llama import _QWeight
+    rng = np.random.default_rng(2)
+    rows, K = 300, 512
+    w = Q.random_quantized(rows, K, Q.Q4_K, rng=rng)
+    W = _QWeight(w, Q.Q4_K, rows, K)
+    monkeypatch.setattr(_QWeight, "SLAB_FLOATS", 100 * K)     # several slabs
+    x = torch.from_numpy(rng.standard_normal((_QWeight.PREFILL_T, K), dtype=np.float32))
+    ref = x @ torch.from_numpy(Q.dequantize(w, Q.Q4_K, rows * K).reshape(rows, K)).T
+    assert torch.allclose(W.mm(x), ref, atol=1e-4)
