@@ -53,16 +53,20 @@ def test_prefix_affinity_and_slack():
     try:
         a = rs.add_request(shared + [1, 2], sp)
         b = rs.add_request(rng.integers(0, cfg.vocab, 70).tolist(), sp)   # other prefix
-        c = rs.add_request(shared + [3], sp)          # same prefix: same replica as a
         assert rs.reqs[a].replica != rs.reqs[b].replica
+        while rs.has_work():                           # a's pages are cached once it is done
+            rs.step(0.1)
+        c = rs.add_request(shared + [3], sp)          # same prefix: same replica as a
         assert rs.reqs[c].replica == rs.reqs[a].replica
-        rs.slack = 0                                   # now load wins over affinity
-        d = rs.add_request(shared + [4], sp)
-        assert rs.reqs[d].replica == rs.reqs[b].replica
         while rs.has_work():
             rs.step(0.1)
-        hits = rs.bm.prefix_hit_tokens
-        assert hits > 0                                # c reused a's cached pages
+        assert rs.bm.prefix_hit_tokens > 0             # c reused a's cached pages
+        rs.slack = 0                                   # now load wins over affinity
+        e = rs.add_request(rng.integers(0, cfg.vocab, 100).tolist(), sp)
+        d = rs.add_request(shared + [4], sp)
+        assert rs.reqs[d].replica != rs.reqs[e].replica
+        while rs.has_work():
+            rs.step(0.1)
     finally:
         rs.close()
 
