@@ -1,8 +1,9 @@
 // Paged attention and the SwiGLU tail on the host CPU.
 //
-// cpu_paged_attention: every (token, KV head) pair is one OpenMP task that
-// serves all the query heads sharing that KV head, so a key/value row is
-// converted to fp32 once per group, not once per query head.  Keys are
+// cpu_paged_attention: every (block of up to 16 tokens of one sequence, KV
+// head) pair is one OpenMP task that serves all the query heads sharing that
+// KV head, so a key/value row is converted to fp32 once per block and group,
+// not once per query head and token.  Keys are
 // walked in 256-key chunks: the chunk's scores for all the group's heads are
 // computed first (scale, optional tanh soft-cap, sliding window and the
 // 64-bit draft-tree visibility mask applied), then one online-softmax update
@@ -110,64 +111,88 @@ __attribute__((always_inline)) inline float kv_load<uint16_t>(const uint16_t* p,
   return half_to_float(p[i]);
 }
 
+constexpr int kTokBlock = 16;   // query tokens of one sequence sharing a task
+
 struct AttnScratch {
   float *s, *acc, *krow, *vrow, *m, *l;
 };
 
-// One (token, KV head) pair: all the query heads of its group.  Inlined into
-// per-ISA clones (below); the OpenMP loop that hands out the pairs stays
-// outside them, since OpenMP outlines its regions before functions are cloned.
-template <typename KV>
+// Tokens t0..t0+nt of one sequence (same block table) and one KV head g: all
+// their query heads share each converted K / V row, so a prefill reads the
+// cache once per block of up to kTokBlock tokens instead of once per token.
+// Each (token, head) row keeps its own key range (window, causal length),
+// tree visibility and online-softmax state.  Inlined into per-ISA clones
+// (below); the OpenMP loop that hands out the tasks stays outside them, since
+// OpenMP outlines its regions before functions are cloned.
+template <typename KV, int NTMAX>
 __attribute__((always_inline)) static inline void attn_task(const AttnArgs& a, const KV* kc,
-                                                            const KV* vc, int t, int g,
+                                                            const KV* vc, int t0, int nt_, int g,
                                                             AttnScratch& w) {
+  const int nt = NTMAX == 1 ? 1 : nt_;   // a lone token (decode) compiles its own loops
   const int nq = a.n_heads, nkv = a.n_kv_heads, d = a.head_dim;
-  const int rep = nq / nkv, ps = a.page_size;
+  const int rep = nq / nkv, ps = a.page_size, R = nt * rep;
   float *s = w.s, *acc = w.acc, *krow = w.krow, *vrow = w.vrow, *m = w.m, *l = w.l;
-  const int Lt = a.seq_lens[t];
-  const int lo = a.window > 0 && Lt > a.window ? Lt - a.window : 0;
-  const float* q = a.q + ((size_t)t * nq + (size_t)g * rep) * d;
-  const int32_t* bt = a.block_table + (size_t)t * a.max_pages;
-  const int ts = a.tree_start ? a.tree_start[t] : 0;
-  const uint64_t tm = a.tree_mask ? (uint64_t)a.tree_mask[t] : 0;
-  for (int i = 0; i < rep * d; ++i) acc[i] = 0.f;
-  for (int h = 0; h < rep; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.f;
+  int lo_t[NTMAX], len_t[NTMAX], ts_t[NTMAX];
+  uint64_t tm_t[NTMAX];
+  int lo = 1 << 30, hi = 0;
+  for (int u = 0; u < nt; ++u) {
+    const int t = t0 + u, Lt = a.seq_lens[t];
+    len_t[u] = Lt;
+    lo_t[u] = a.window > 0 && Lt > a.window ? Lt - a.window : 0;
+    ts_t[u] = a.tree_start ? a.tree_start[t] : 0;
+    tm_t[u] = a.tree_mask ? (uint64_t)a.tree_mask[t] : 0;
+    lo = lo_t[u] < lo ? lo_t[u] : lo;
+    hi = Lt > hi ? Lt : hi;
   }
-  for (int c0 = lo; c0 < Lt; c0 += kChunk) {
-    const int nc = Lt - c0 < kChunk ? Lt - c0 : kChunk;
+  const int32_t* bt = a.block_table + (size_t)t0 * a.max_pages;
+  for (int i = 0; i < R * d; ++i) acc[i] = 0.f;
+  for (int r = 0; r < R; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+  }
+  for (int c0 = lo; c0 < hi; c0 += kChunk) {
+    const int nc = hi - c0 < kChunk ? hi - c0 : kChunk;
     for (int j = 0; j < nc; ++j) {
       const int key = c0 + j;
-      bool vis = true;
-      if (a.tree_mask) {
-        const int rel = key - ts;
-        vis = rel < 0 || (rel < 64 && ((tm >> rel) & 1));
+      bool any = false;
+      bool vis[NTMAX];
+      for (int u = 0; u < nt; ++u) {
+        bool v = key >= lo_t[u] && key < len_t[u];
+        if (v && a.tree_mask) {
+          const int rel = key - ts_t[u];
+          v = rel < 0 || (rel < 64 && ((tm_t[u] >> rel) & 1));
+        }
+        vis[u] = v;
+        any |= v;
       }
-      if (!vis) {
-        for (int h = 0; h < rep; ++h) s[(size_t)h * kChunk + j] = -INFINITY;
-        continue;
-      }
-      const size_t off =
-          (((size_t)bt[key / ps] * nkv + g) * ps + (size_t)(key % ps)) * (size_t)d;
+      if (any) {
+        const size_t off =
+            (((size_t)bt[key / ps] * nkv + g) * ps + (size_t)(key % ps)) * (size_t)d;
 #pragma omp simd
-      for (int i = 0; i < d; ++i) krow[i] = kv_load(kc + off, i);
-      for (int h = 0; h < rep; ++h) {
-        const float* qh = q + (size_t)h * d;
-        float dot = 0.f;
+        for (int i = 0; i < d; ++i) krow[i] = kv_load(kc + off, i);
+      }
+      for (int u = 0; u < nt; ++u) {
+        const float* qt = a.q + ((size_t)(t0 + u) * nq + (size_t)g * rep) * d;
+        for (int h = 0; h < rep; ++h) {
+          float dot = -INFINITY;
+          if (vis[u]) {
+            const float* qh = qt + (size_t)h * d;
+            dot = 0.f;
 #pragma omp simd reduction(+ : dot)
-        for (int i = 0; i < d; ++i) dot += qh[i] * krow[i];
-        dot *= a.scale;
-        if (a.softcap > 0.f) dot = a.softcap * std::tanh(dot / a.softcap);
-        s[(size_t)h * kChunk + j] = dot;
+            for (int i = 0; i < d; ++i) dot += qh[i] * krow[i];
+            dot *= a.scale;
+            if (a.softcap > 0.f) dot = a.softcap * std::tanh(dot / a.softcap);
+          }
+          s[(size_t)(u * rep + h) * kChunk + j] = dot;
+        }
       }
     }
-    for (int h = 0; h < rep; ++h) {
-      float* sh = s + (size_t)h * kChunk;
-      float mx = m[h];
+    for (int r = 0; r < R; ++r) {
+      float* sh = s + (size_t)r * kChunk;
+      float mx = m[r];
       for (int j = 0; j < nc; ++j) mx = sh[j] > mx ? sh[j] : mx;
       if (mx == -INFINITY) continue;  // nothing visible yet
-      const float corr = m[h] == -INFINITY ? 0.f : exp_fast(m[h] - mx);
+      const float corr = m[r] == -INFINITY ? 0.f : exp_fast(m[r] - mx);
       float sum = 0.f;
 #pragma omp simd reduction(+ : sum)
       for (int j = 0; j < nc; ++j) {
@@ -175,77 +200,97 @@ __attribute__((always_inline)) static inline void attn_task(const AttnArgs& a, c
         sh[j] = p;
         sum += p;
       }
-      l[h] = l[h] * corr + sum;
-      m[h] = mx;
-      float* ah = acc + (size_t)h * d;
+      l[r] = l[r] * corr + sum;
+      m[r] = mx;
+      float* ah = acc + (size_t)r * d;
       for (int i = 0; i < d; ++i) ah[i] *= corr;
     }
     for (int j = 0; j < nc; ++j) {
+      bool any = false;
+      for (int r = 0; r < R; ++r) any |= s[(size_t)r * kChunk + j] > 0.f;
+      if (!any) continue;
       const int key = c0 + j;
       const size_t off =
           (((size_t)bt[key / ps] * nkv + g) * ps + (size_t)(key % ps)) * (size_t)d;
-      bool any = false;
-      for (int h = 0; h < rep; ++h) any |= s[(size_t)h * kChunk + j] > 0.f;
-      if (!any) continue;
 #pragma omp simd
       for (int i = 0; i < d; ++i) vrow[i] = kv_load(vc + off, i);
-      for (int h = 0; h < rep; ++h) {
-        const float p = s[(size_t)h * kChunk + j];
+      for (int r = 0; r < R; ++r) {
+        const float p = s[(size_t)r * kChunk + j];
         if (p == 0.f) continue;
-        float* ah = acc + (size_t)h * d;
+        float* ah = acc + (size_t)r * d;
 #pragma omp simd
         for (int i = 0; i < d; ++i) ah[i] += p * vrow[i];
       }
     }
   }
-  for (int h = 0; h < rep; ++h) {
-    float den = l[h], sc = 1.f;
-    if (a.sinks) {
-      const float sk = a.sinks[g * rep + h];
-      const float mx = m[h] > sk ? m[h] : sk;
-      sc = m[h] == -INFINITY ? 0.f : exp_fast(m[h] - mx);
-      den = l[h] * sc + exp_fast(sk - mx);
+  for (int u = 0; u < nt; ++u)
+    for (int h = 0; h < rep; ++h) {
+      const int r = u * rep + h;
+      float den = l[r], sc = 1.f;
+      if (a.sinks) {
+        const float sk = a.sinks[g * rep + h];
+        const float mx = m[r] > sk ? m[r] : sk;
+        sc = m[r] == -INFINITY ? 0.f : exp_fast(m[r] - mx);
+        den = l[r] * sc + exp_fast(sk - mx);
+      }
+      const float inv = den > 0.f ? sc / den : 0.f;
+      float* o = a.out + ((size_t)(t0 + u) * nq + (size_t)g * rep + h) * d;
+      const float* ah = acc + (size_t)r * d;
+      for (int i = 0; i < d; ++i) o[i] = ah[i] * inv;
     }
-    const float inv = den > 0.f ? sc / den : 0.f;
-    float* o = a.out + ((size_t)t * nq + (size_t)g * rep + h) * d;
-    const float* ah = acc + (size_t)h * d;
-    for (int i = 0; i < d; ++i) o[i] = ah[i] * inv;
-  }
 }
 
 SWARM_CLONES static void attn_task_f16(const AttnArgs& a, const uint16_t* k, const uint16_t* v,
-                                       int t, int g, AttnScratch& w) {
-  attn_task(a, k, v, t, g, w);
+                                       int t0, int nt, int g, AttnScratch& w) {
+  if (nt == 1)
+    attn_task<uint16_t, 1>(a, k, v, t0, 1, g, w);
+  else
+    attn_task<uint16_t, kTokBlock>(a, k, v, t0, nt, g, w);
 }
 
-SWARM_CLONES static void attn_task_f32(const AttnArgs& a, const float* k, const float* v, int t,
-                                       int g, AttnScratch& w) {
-  attn_task(a, k, v, t, g, w);
+SWARM_CLONES static void attn_task_f32(const AttnArgs& a, const float* k, const float* v, int t0,
+                                       int nt, int g, AttnScratch& w) {
+  if (nt == 1)
+    attn_task<float, 1>(a, k, v, t0, 1, g, w);
+  else
+    attn_task<float, kTokBlock>(a, k, v, t0, nt, g, w);
 }
 
 int cpu_paged_attention(const AttnArgs& a, const void* k_cache, const void* v_cache,
                         bool kv_fp16) {
   if (a.n_heads % a.n_kv_heads != 0 || a.head_dim <= 0 || a.page_size <= 0) return -1;
   const int rep = a.n_heads / a.n_kv_heads, d = a.head_dim;
+  // blocks of consecutive tokens that read the same pages (one sequence)
+  std::vector<int> starts;
+  for (int t = 0; t < a.n_tokens; ++t) {
+    const bool same = !starts.empty() && t - starts.back() < kTokBlock &&
+                      std::memcmp(a.block_table + (size_t)t * a.max_pages,
+                                  a.block_table + (size_t)starts.back() * a.max_pages,
+                                  sizeof(int32_t) * (size_t)a.max_pages) == 0;
+    if (!same) starts.push_back(t);
+  }
+  starts.push_back(a.n_tokens);
+  const int nb = (int)starts.size() - 1, R = kTokBlock * rep;
 #pragma omp parallel
   {
-    std::vector<float> buf((size_t)rep * kChunk + (size_t)rep * d + 2 * (size_t)d + 2 * rep);
+    std::vector<float> buf((size_t)R * kChunk + (size_t)R * d + 2 * (size_t)d + 2 * (size_t)R);
     AttnScratch w;
     w.s = buf.data();
-    w.acc = w.s + (size_t)rep * kChunk;
-    w.krow = w.acc + (size_t)rep * d;
+    w.acc = w.s + (size_t)R * kChunk;
+    w.krow = w.acc + (size_t)R * d;
     w.vrow = w.krow + d;
     w.m = w.vrow + d;
-    w.l = w.m + rep;
+    w.l = w.m + R;
 #pragma omp for collapse(2) schedule(dynamic)
-    for (int t = 0; t < a.n_tokens; ++t)
+    for (int b = 0; b < nb; ++b)
       for (int g = 0; g < a.n_kv_heads; ++g) {
+        const int t0 = starts[b], nt = starts[b + 1] - starts[b];
         if (kv_fp16)
           attn_task_f16(a, static_cast<const uint16_t*>(k_cache),
-                        static_cast<const uint16_t*>(v_cache), t, g, w);
+                        static_cast<const uint16_t*>(v_cache), t0, nt, g, w);
         else
           attn_task_f32(a, static_cast<const float*>(k_cache), static_cast<const float*>(v_cache),
-                        t, g, w);
+                        t0, nt, g, w);
       }
   }
   return 0;

@@ -117,3 +117,33 @@ def test_cpu_attention_reads_every_fp16_value():
     bt = np.arange(n, dtype=np.int32).reshape(n, 1)
     out = _native.cpu_paged_attention(q, K, V, bt, np.ones(n, np.int32), 1.0)
     assert np.array_equal(out.reshape(-1), V.reshape(-1).astype(np.float32))
+
+
+@pytest.mark.parametrize("window,tree,sinks", [(0, False, False), (40, False, True), (0, True, False)])
+def test_cpu_attention_prefill_blocks(window, tree, sinks):
+    """Tokens of one sequence (one block table, causal lengths) share tasks in
+    blocks of 16: per-token key ranges, windows, tree masks and sinks kept."""
+    g = torch.Generator().manual_seed(5)
+    T, nq, nkv, d, ps = 37, 8, 2, 64, 16
+    pages = (T + ps - 1) // ps + 1
+    K = torch.randn(pages, nkv, ps, d, generator=g).half()
+    V = torch.randn(pages, nkv, ps, d, generator=g).half()
+    bt = torch.randperm(pages, generator=g).int().repeat(T, 1)
+    lens = torch.arange(1, T + 1, dtype=torch.int32)
+    q = torch.randn(T, nq, d, generator=g)
+    kw, ref_kw = {}, {}
+    if window:
+        kw["window"] = ref_kw["window"] = window
+    if tree:
+        ts = np.full(T, 30, np.int32)
+        masks = np.random.default_rng(1).integers(0, 2 ** 20, size=T, dtype=np.int64) | 1
+        kw.update(tree_start=ts, tree_mask=masks)
+        ref_kw.update(tree_start=torch.from_numpy(ts), tree_mask=torch.from_numpy(masks))
+    if sinks:
+        sk = torch.randn(nq, generator=g)
+        kw["sinks"], ref_kw["sinks"] = sk.numpy(), sk
+    out = _native.cpu_paged_attention(q.numpy(), K.numpy(), V.numpy(), bt.numpy(), lens.numpy(),
+                                      0.125, **kw)
+    ref = _reference(q, K, V, bt, lens, 0.125, **ref_kw)
+    ok = ~torch.isnan(ref)
+    assert np.abs(out[ok.numpy()] - ref[ok].numpy()).max() < 1e-4
