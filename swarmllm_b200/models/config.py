@@ -100,6 +100,7 @@ class ModelConfig:
     moe_scale: float = 1.0              # sigmoid gating: routed-weight multiplier
     moe_dense_layers: int = 0           # leading layers with a dense FFN (size `ffn`)
     shared_expert_gated: bool = True    # a sigmoid gate (ffn_gate_inp_shexp) on the shared expert
+    mtp_layers: int = 0                 # next-token-prediction blocks after the trunk (blk.{n_layers})
     swiglu_limit: float = 0.0           # gpt-oss clamped SwiGLU (7.0)
     swiglu_alpha: float = 1.702
     # hybrid linear attention (gated DeltaNet)
@@ -130,7 +131,7 @@ class ModelConfig:
         return self.rope_dim or self.head_dim
 
     def is_swa(self, layer: int) -> bool:
-        if not self.sliding_window:
+        if not self.sliding_window or self.is_mtp_block(layer):   # MTP blocks attend fully
             return False
         if self.swa_pattern:
             return (layer + 1) % self.swa_pattern != 0
@@ -172,8 +173,13 @@ class ModelConfig:
             return 2
         return 1 if self.moe_softmax_after_topk else 0
 
+    def is_mtp_block(self, layer: int) -> bool:
+        """A next-token-prediction block (after the trunk): full attention."""
+        return self.mtp_layers > 0 and layer >= self.n_layers
+
     def is_linear_attn(self, layer: int) -> bool:
-        return bool(self.full_attn_interval) and (layer + 1) % self.full_attn_interval != 0
+        return (bool(self.full_attn_interval) and not self.is_mtp_block(layer)
+                and (layer + 1) % self.full_attn_interval != 0)
 
     def is_moe(self, layer: int) -> bool:
         return self.n_experts > 0
@@ -380,12 +386,17 @@ def apply_family(cfg: ModelConfig, md: dict | None = None) -> ModelConfig:
             n_sh = int(g("expert_shared_count", 1 if cfg.shared_expert_ffn else 0))
             cfg.shared_expert_ffn = n_sh * cfg.expert_ffn if n_sh else 0
             # next-token-prediction blocks follow the model's own layers
-            cfg.n_layers -= int(g("nextn_predict_layers", 0))
+            cfg.mtp_layers = int(g("nextn_predict_layers", 0))
+            cfg.n_layers -= cfg.mtp_layers
     if fam == "gpt-oss":
         cfg.rope_neox, cfg.attn_sinks, cfg.attn_bias, cfg.swa_every = True, True, True, 2
         cfg.swiglu_limit = cfg.swiglu_limit or 7.0
     if fam in ("qwen3next", "qwen35", "qwen35moe"):
         cfg.rope_neox, cfg.qk_norm, cfg.attn_output_gate = True, True, True
+    if fam in ("qwen35", "qwen35moe") and md is not None:
+        # Qwen 3.5 files count only the trunk in block_count; the block after it
+        # (blk.{block_count}) is the next-token-prediction head
+        cfg.mtp_layers = int(g("nextn_predict_layers", cfg.mtp_layers))
     return cfg
 
 
@@ -393,7 +404,7 @@ def to_gguf_metadata(cfg: ModelConfig) -> dict:
     a = _ARCH_KEYS[cfg.arch]
     md = {
         "general.name": cfg.name,
-        f"{a}.block_count": cfg.n_layers,
+        f"{a}.block_count": cfg.n_layers + (cfg.mtp_layers if cfg.arch == "glm4moe" else 0),
         f"{a}.embedding_length": cfg.hidden,
         f"{a}.feed_forward_length": cfg.ffn,
         f"{a}.attention.head_count": cfg.n_heads,
@@ -424,6 +435,8 @@ def to_gguf_metadata(cfg: ModelConfig) -> dict:
             md[f"{a}.expert_shared_count"] = cfg.shared_expert_ffn // max(1, cfg.expert_ffn)
         if cfg.moe_dense_layers:
             md[f"{a}.leading_dense_block_count"] = cfg.moe_dense_layers
+    if cfg.mtp_layers:
+        md[f"{a}.nextn_predict_layers"] = cfg.mtp_layers
     if cfg.sliding_window:
         md[f"{a}.attention.sliding_window"] = cfg.sliding_window
     if cfg.attn_softcap:

@@ -13,9 +13,10 @@ as the reference reads them in src/inference/layers/qwen35.rs:116-230):
   f % n_k -- and separate ``ssm_beta`` / ``ssm_alpha`` tensors.  Kernel head
   g = kh * r + j is file head j * n_k + kh.
 
-GLM-4.5 (``glm4moe``) files name the norm before the feed-forward
-``post_attention_norm``; the engine calls it ``ffn_norm`` like every other
-family's, so it is renamed on the way in and out.
+GLM-4.5 (``glm4moe``), gpt-oss and the Qwen 3.5 / Qwen3-Next hybrids name
+the norm before the feed-forward ``post_attention_norm`` (llama.cpp reads it
+as ``attn_post_norm`` on the FFN input); the engine calls it ``ffn_norm``
+like every other family's, so it is renamed on the way in and out.
 
 ``to_kernel`` turns a file tensor into the kernels' order when a GGUF is read
 (whole rows move, still quantized; ``ssm_out``'s value heads are columns,
@@ -32,7 +33,8 @@ from ..gguf import quants as Q
 HYBRID_FAMILIES = ("qwen3next", "qwen35", "qwen35moe")
 TILED_FAMILIES = ("qwen35", "qwen35moe")
 # engine name suffix -> file name suffix, per family
-RENAMES = {"glm4moe": {"ffn_norm.weight": "post_attention_norm.weight"}}
+RENAMES = {a: {"ffn_norm.weight": "post_attention_norm.weight"}
+           for a in ("glm4moe", "gpt-oss", "qwen3next", "qwen35", "qwen35moe")}
 LAYOUT_FAMILIES = HYBRID_FAMILIES + tuple(RENAMES)
 
 
@@ -40,6 +42,14 @@ def file_name(arch: str, name: str) -> str:
     for a, b in RENAMES.get(arch, {}).items():
         if name.endswith("." + a):
             return name[: -len(a)] + b
+    return name
+
+
+def engine_name(arch: str, name: str) -> str:
+    """The inverse of file_name."""
+    for a, b in RENAMES.get(arch, {}).items():
+        if name.endswith("." + b):
+            return name[: -len(b)] + a
     return name
 
 
@@ -111,11 +121,9 @@ def to_kernel(cfg, name: str, fetch):
     returns a file tensor as (numpy uint8 bytes, qtype, shape)."""
     arch = cfg.arch
     parts = kernel_name(arch, name)
-    if arch in RENAMES:
-        return fetch(parts[0])
     if arch not in HYBRID_FAMILIES or ".ssm_" not in name and not name.endswith(
             ("attn_qkv.weight", "attn_gate.weight")):
-        return fetch(name)
+        return fetch(file_name(arch, name))
     nk, nv, d = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
     layer = int(name.split(".")[1])
     if not cfg.is_linear_attn(layer):
@@ -149,18 +157,14 @@ def to_kernel(cfg, name: str, fetch):
 
 def file_specs(cfg, specs):
     """Kernel-order tensor specs -> the family's file tensors (name, shape, qtype)."""
-    if cfg.arch in RENAMES:
-        return [(file_name(cfg.arch, n), shape, qt) for n, shape, qt in specs]
-    if cfg.arch not in TILED_FAMILIES:
-        return list(specs)
     out = []
     for name, shape, qt in specs:
-        if name.endswith("ssm_ba.weight"):
+        if cfg.arch in TILED_FAMILIES and name.endswith("ssm_ba.weight"):
             half = (shape[0] // 2, shape[1])
             for n in kernel_name(cfg.arch, name):
                 out.append((n, half, qt))
         else:
-            out.append((name, shape, qt))
+            out.append((file_name(cfg.arch, name), shape, qt))
     return out
 
 
@@ -169,12 +173,7 @@ def to_file(cfg, name: str, shape, qt: int, kernel_get):
     (`kernel_get(n)` -> numpy uint8 bytes): the inverse of to_kernel, at the
     float level for column moves (the random-init writer's use)."""
     arch = cfg.arch
-    if arch in RENAMES:
-        inv_names = {b: a for a, b in RENAMES[arch].items()}
-        for b, a in inv_names.items():
-            if name.endswith("." + b):
-                return kernel_get(name[: -len(b)] + a)
-        return kernel_get(name)
+    name = engine_name(arch, name)
     if arch not in HYBRID_FAMILIES or ".ssm_" not in name and not name.endswith(
             ("attn_qkv.weight", "attn_gate.weight")):
         return kernel_get(name)

@@ -708,29 +708,7 @@ class LlamaCPU:
                 continue
             L.kv_idx = n_attn
             n_attn += 1
-            qr = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
-            if cfg.fused_qkv:
-                wqkv = lw(b + "attn_qkv.weight")
-                L.wq, L.wk, L.wv = wqkv[:qr], wqkv[qr:qr + cfg.kv_dim], wqkv[qr + cfg.kv_dim:]
-                if cfg.attn_bias:
-                    bqkv = dq(b + "attn_qkv.bias")
-                    L.bq, L.bk, L.bv = bqkv[:qr], bqkv[qr:qr + cfg.kv_dim], bqkv[qr + cfg.kv_dim:]
-                else:
-                    L.bq = L.bk = L.bv = None
-            else:
-                L.wq, L.wk, L.wv = lw(b + "attn_q.weight"), lw(b + "attn_k.weight"), lw(b + "attn_v.weight")
-                L.bq = dq(b + "attn_q.bias") if cfg.attn_bias else None
-                L.bk = dq(b + "attn_k.bias") if cfg.attn_bias else None
-                L.bv = dq(b + "attn_v.bias") if cfg.attn_bias else None
-            L.wo = lw(b + "attn_output.weight")
-            L.bo = dq(b + "attn_output.bias") if cfg.has_out_bias else None
-            L.post_attn = dq(b + "post_attention_norm.weight") if cfg.post_norms else None
-            L.post_ffn = dq(b + "post_ffw_norm.weight") if cfg.post_norms else None
-            L.local_rope = bool(cfg.rope_local_theta) and cfg.is_swa(i)
-            L.q_norm = dq(b + "attn_q_norm.weight") if cfg.qk_norm else None
-            L.k_norm = dq(b + "attn_k_norm.weight") if cfg.qk_norm else None
-            L.sinks = dq(b + "attn_sinks.weight") if cfg.attn_sinks else None
-            L.window = cfg.sliding_window if cfg.is_swa(i) else 0
+            self._load_attn(L, i, b, dq, lw)
             self._load_ffn_cpu(L, b, dq, lw)
             self.layers.append(L)
         self.n_kv_layers, self.n_lin_layers = n_attn, n_lin
@@ -744,6 +722,33 @@ class LlamaCPU:
         self.scale = cfg.softmax_scale
 
     linear_state_spec = LlamaGPU.linear_state_spec
+
+    def _load_attn(self, L, i, b, dq, lw):
+        """A full-attention layer's weights (projections, biases, norms, sinks)."""
+        cfg = self.cfg
+        qr = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
+        if cfg.fused_qkv:
+            wqkv = lw(b + "attn_qkv.weight")
+            L.wq, L.wk, L.wv = wqkv[:qr], wqkv[qr:qr + cfg.kv_dim], wqkv[qr + cfg.kv_dim:]
+            if cfg.attn_bias:
+                bqkv = dq(b + "attn_qkv.bias")
+                L.bq, L.bk, L.bv = bqkv[:qr], bqkv[qr:qr + cfg.kv_dim], bqkv[qr + cfg.kv_dim:]
+            else:
+                L.bq = L.bk = L.bv = None
+        else:
+            L.wq, L.wk, L.wv = lw(b + "attn_q.weight"), lw(b + "attn_k.weight"), lw(b + "attn_v.weight")
+            L.bq = dq(b + "attn_q.bias") if cfg.attn_bias else None
+            L.bk = dq(b + "attn_k.bias") if cfg.attn_bias else None
+            L.bv = dq(b + "attn_v.bias") if cfg.attn_bias else None
+        L.wo = lw(b + "attn_output.weight")
+        L.bo = dq(b + "attn_output.bias") if cfg.has_out_bias else None
+        L.post_attn = dq(b + "post_attention_norm.weight") if cfg.post_norms else None
+        L.post_ffn = dq(b + "post_ffw_norm.weight") if cfg.post_norms else None
+        L.local_rope = bool(cfg.rope_local_theta) and cfg.is_swa(i)
+        L.q_norm = dq(b + "attn_q_norm.weight") if cfg.qk_norm else None
+        L.k_norm = dq(b + "attn_k_norm.weight") if cfg.qk_norm else None
+        L.sinks = dq(b + "attn_sinks.weight") if cfg.attn_sinks else None
+        L.window = cfg.sliding_window if cfg.is_swa(i) else 0
 
     def _load_ffn_cpu(self, L, b, dq, lw=None):
         cfg = self.cfg
@@ -977,10 +982,12 @@ class LlamaCPU:
             y = y + gate * self._mm(self._glu(self._mm(x, L.sg), self._mm(x, L.su)), L.sd)
         return y
 
-    def forward(self, b: StepBatch, kv: PagedKVCache, ctx=None, h_in=None) -> torch.Tensor:
+    def forward(self, b: StepBatch, kv: PagedKVCache, ctx=None, h_in=None,
+                want_hidden: bool = False) -> torch.Tensor:
+        """Logits of the sample rows (the last stage), or the residual stream
+        (other stages).  want_hidden: also the output-normed hidden state of
+        every row, (logits, hidden) -- what a next-token-prediction head reads."""
         cfg = self.cfg
-        N = b.tokens.shape[0]
-        nq, nkv, d = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         h = self.embd[b.tokens.long()].clone() if self.first else h_in.to(self.dtype).clone()
         if self.first and cfg.embed_scale:
             h = h * cfg.embed_scale
@@ -996,50 +1003,62 @@ class LlamaCPU:
                 x = self._norm(h, L.ffn_norm)
                 h = h + self._ffn(L, x)
                 continue
-            li = self.kv_off + L.kv_idx
-            layer = self.lo + j
-            mm = self._mm
-            q = self._lora_cpu(layer, "attn_q", x, mm(x, L.wq), b)
-            k = self._lora_cpu(layer, "attn_k", x, mm(x, L.wk), b)
-            v = self._lora_cpu(layer, "attn_v", x, mm(x, L.wv), b)
-            gate = None
-            if cfg.attn_output_gate:
-                qg = q.view(N, nq, 2 * d)
-                q, gate = qg[..., :d], torch.sigmoid(qg[..., d:]).reshape(N, nq * d)
-            if L.bq is not None:
-                q, k, v = q + L.bq, k + L.bk, v + L.bv
-            q, k, v = q.reshape(N, nq, d), k.view(N, nkv, d), v.view(N, nkv, d)
-            if L.q_norm is not None:
-                q, k = self._norm(q, L.q_norm), self._norm(k, L.k_norm)
-            q, k = self._rope(q, b.positions, L.local_rope), self._rope(k, b.positions, L.local_rope)
-            K, V = kv.k(li), kv.v(li)
-            K[pages, :, offs, :] = k.to(K.dtype)
-            V[pages, :, offs, :] = v.to(V.dtype)
-            if self.native:
-                att = self._attention_native(L, q, K, V, b)
-            else:
-                att = self._attention(L, q, K, V, b)
-            a = att.view(N, nq * d)
-            if gate is not None:
-                a = a * gate
-            o = self._lora_cpu(layer, "attn_output", a, mm(a, L.wo), b)
-            if L.bo is not None:
-                o = o + L.bo
-            if L.post_attn is not None:
-                o = self._norm(o, L.post_attn)
-            h = h + o
-            x = self._norm(h, L.ffn_norm)
-            f = self._ffn(L, x, layer, b)
-            if L.post_ffn is not None:
-                f = self._norm(f, L.post_ffn)
-            h = h + f
+            h = self._attn_layer(L, self.lo + j, h, x, b, kv, self.kv_off + L.kv_idx, pages, offs)
         if not self.last:
             return h
         x = self._norm(h[b.sample_rows.long()], self.out_norm)
-        logits = self._mm(x, self.head)
-        if cfg.final_softcap:
-            logits = cfg.final_softcap * torch.tanh(logits / cfg.final_softcap)
+        logits = self._logits(x)
+        if want_hidden:
+            return logits, self._norm(h, self.out_norm)
         return logits
+
+    def _logits(self, x):
+        logits = self._mm(x, self.head)
+        if self.cfg.final_softcap:
+            logits = self.cfg.final_softcap * torch.tanh(logits / self.cfg.final_softcap)
+        return logits
+
+    def _attn_layer(self, L, layer, h, x, b, kv, li, pages, offs):
+        """One full-attention decoder layer: x = attn_norm(h) in, the new
+        residual out (attention, output gate, post-norms, FFN)."""
+        cfg = self.cfg
+        N = x.shape[0]
+        nq, nkv, d = cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        mm = self._mm
+        q = self._lora_cpu(layer, "attn_q", x, mm(x, L.wq), b)
+        k = self._lora_cpu(layer, "attn_k", x, mm(x, L.wk), b)
+        v = self._lora_cpu(layer, "attn_v", x, mm(x, L.wv), b)
+        gate = None
+        if cfg.attn_output_gate:
+            qg = q.view(N, nq, 2 * d)
+            q, gate = qg[..., :d], torch.sigmoid(qg[..., d:]).reshape(N, nq * d)
+        if L.bq is not None:
+            q, k, v = q + L.bq, k + L.bk, v + L.bv
+        q, k, v = q.reshape(N, nq, d), k.view(N, nkv, d), v.view(N, nkv, d)
+        if L.q_norm is not None:
+            q, k = self._norm(q, L.q_norm), self._norm(k, L.k_norm)
+        q, k = self._rope(q, b.positions, L.local_rope), self._rope(k, b.positions, L.local_rope)
+        K, V = kv.k(li), kv.v(li)
+        K[pages, :, offs, :] = k.to(K.dtype)
+        V[pages, :, offs, :] = v.to(V.dtype)
+        if self.native:
+            att = self._attention_native(L, q, K, V, b)
+        else:
+            att = self._attention(L, q, K, V, b)
+        a = att.view(N, nq * d)
+        if gate is not None:
+            a = a * gate
+        o = self._lora_cpu(layer, "attn_output", a, mm(a, L.wo), b)
+        if L.bo is not None:
+            o = o + L.bo
+        if L.post_attn is not None:
+            o = self._norm(o, L.post_attn)
+        h = h + o
+        x = self._norm(h, L.ffn_norm)
+        f = self._ffn(L, x, layer, b)
+        if L.post_ffn is not None:
+            f = self._norm(f, L.post_ffn)
+        return h + f
 
     def _attention(self, L, q, K, V, b):
         """The fp32 oracle: per row, gather its keys and take a plain softmax."""

@@ -24,6 +24,80 @@ from .config import ModelConfig, from_gguf_metadata, to_gguf_metadata
 from .layout import LAYOUT_FAMILIES, file_specs, kernel_name, to_file, to_kernel
 
 
+def _layer_specs(cfg: ModelConfig, i: int, wq: int, xq: int) -> list:
+    """(name, shape, qtype) of layer i's tensors."""
+    H = cfg.hidden
+    specs = []
+    b = f"blk.{i}."
+    specs.append((b + "attn_norm.weight", (H,), Q.F32))
+    if cfg.is_linear_attn(i):
+        nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
+        qkv = 2 * nk * dh + nv * dh
+        specs += [(b + "attn_qkv.weight", (qkv, H), wq),
+                  (b + "attn_gate.weight", (nv * dh, H), wq),
+                  (b + "ssm_ba.weight", (2 * nv, H), Q.F32),
+                  (b + "ssm_conv1d.weight", (qkv, cfg.ssm_conv_kernel), Q.F32),
+                  (b + "ssm_dt.bias", (nv,), Q.F32),
+                  (b + "ssm_a", (nv,), Q.F32),
+                  (b + "ssm_norm.weight", (dh,), Q.F32),
+                  (b + "ssm_out.weight", (H, nv * dh), wq)]
+    else:
+        qrows = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
+        if cfg.fused_qkv:
+            specs.append((b + "attn_qkv.weight", (qrows + 2 * cfg.kv_dim, H), wq))
+            if cfg.attn_bias:
+                specs.append((b + "attn_qkv.bias", (qrows + 2 * cfg.kv_dim,), Q.F32))
+        else:
+            specs += [(b + "attn_q.weight", (qrows, H), wq),
+                      (b + "attn_k.weight", (cfg.kv_dim, H), wq),
+                      (b + "attn_v.weight", (cfg.kv_dim, H), wq)]
+            if cfg.attn_bias:
+                specs += [(b + "attn_q.bias", (cfg.q_dim,), Q.F32),
+                          (b + "attn_k.bias", (cfg.kv_dim,), Q.F32),
+                          (b + "attn_v.bias", (cfg.kv_dim,), Q.F32)]
+        specs.append((b + "attn_output.weight", (H, cfg.q_dim), wq))
+        if cfg.has_out_bias:
+            specs.append((b + "attn_output.bias", (H,), Q.F32))
+        if cfg.post_norms:
+            specs.append((b + "post_attention_norm.weight", (H,), Q.F32))
+        if cfg.qk_norm:
+            specs += [(b + "attn_q_norm.weight", (cfg.head_dim,), Q.F32),
+                      (b + "attn_k_norm.weight", (cfg.head_dim,), Q.F32)]
+        if cfg.attn_sinks:
+            specs.append((b + "attn_sinks.weight", (cfg.n_heads,), Q.F32))
+    specs.append((b + "ffn_norm.weight", (H,), Q.F32))
+    if cfg.is_moe_layer(i):
+        E, F = cfg.n_experts, cfg.expert_ffn
+        specs += [(b + "ffn_gate_inp.weight", (E, H), Q.F32),
+                  (b + "ffn_gate_exps.weight", (E, F, H), xq),
+                  (b + "ffn_up_exps.weight", (E, F, H), xq),
+                  (b + "ffn_down_exps.weight", (E, H, F), xq)]
+        if cfg.arch == "gpt-oss":
+            specs += [(b + "ffn_gate_inp.bias", (E,), Q.F32),
+                      (b + "ffn_gate_exps.bias", (E, F), Q.F32),
+                      (b + "ffn_up_exps.bias", (E, F), Q.F32),
+                      (b + "ffn_down_exps.bias", (E, H), Q.F32)]
+        if cfg.moe_gating == "sigmoid":
+            specs.append((b + "exp_probs_b.bias", (E,), Q.F32))
+        if cfg.shared_expert_ffn:
+            S = cfg.shared_expert_ffn
+            specs += [(b + "ffn_gate_shexp.weight", (S, H), wq),
+                      (b + "ffn_up_shexp.weight", (S, H), wq),
+                      (b + "ffn_down_shexp.weight", (H, S), wq)]
+            if cfg.shared_expert_gated:
+                specs.append((b + "ffn_gate_inp_shexp.weight", (H,), Q.F32))
+    elif cfg.fused_gate_up:
+        specs += [(b + "ffn_up.weight", (2 * cfg.ffn, H), wq),
+                  (b + "ffn_down.weight", (H, cfg.ffn), wq)]
+    else:
+        specs += [(b + "ffn_gate.weight", (cfg.ffn, H), wq),
+                  (b + "ffn_up.weight", (cfg.ffn, H), wq),
+                  (b + "ffn_down.weight", (H, cfg.ffn), wq)]
+    if cfg.post_norms and not cfg.is_linear_attn(i):
+        specs.append((b + "post_ffw_norm.weight", (H,), Q.F32))
+    return specs
+
+
 def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
     """(name, shape, qtype) of every tensor of a model (llama.cpp names)."""
     wq = Q.NAME_TO_TYPE[cfg.weight_qtype]
@@ -33,73 +107,16 @@ def tensor_specs(cfg: ModelConfig) -> list[tuple[str, tuple, int]]:
     H = cfg.hidden
     specs = [("token_embd.weight", (cfg.vocab, H), eq)]
     for i in range(cfg.n_layers):
+        specs += _layer_specs(cfg, i, wq, xq)
+    for i in range(cfg.n_layers, cfg.n_layers + cfg.mtp_layers):
+        # a next-token-prediction block: a full-attention layer whose input is
+        # eh_proj([enorm(embedding of the next token) | hnorm(trunk hidden)])
         b = f"blk.{i}."
-        specs.append((b + "attn_norm.weight", (H,), Q.F32))
-        if cfg.is_linear_attn(i):
-            nk, nv, dh = cfg.ssm_k_heads, cfg.ssm_v_heads, cfg.ssm_head_dim
-            qkv = 2 * nk * dh + nv * dh
-            specs += [(b + "attn_qkv.weight", (qkv, H), wq),
-                      (b + "attn_gate.weight", (nv * dh, H), wq),
-                      (b + "ssm_ba.weight", (2 * nv, H), Q.F32),
-                      (b + "ssm_conv1d.weight", (qkv, cfg.ssm_conv_kernel), Q.F32),
-                      (b + "ssm_dt.bias", (nv,), Q.F32),
-                      (b + "ssm_a", (nv,), Q.F32),
-                      (b + "ssm_norm.weight", (dh,), Q.F32),
-                      (b + "ssm_out.weight", (H, nv * dh), wq)]
-        else:
-            qrows = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
-            if cfg.fused_qkv:
-                specs.append((b + "attn_qkv.weight", (qrows + 2 * cfg.kv_dim, H), wq))
-                if cfg.attn_bias:
-                    specs.append((b + "attn_qkv.bias", (qrows + 2 * cfg.kv_dim,), Q.F32))
-            else:
-                specs += [(b + "attn_q.weight", (qrows, H), wq),
-                          (b + "attn_k.weight", (cfg.kv_dim, H), wq),
-                          (b + "attn_v.weight", (cfg.kv_dim, H), wq)]
-                if cfg.attn_bias:
-                    specs += [(b + "attn_q.bias", (cfg.q_dim,), Q.F32),
-                              (b + "attn_k.bias", (cfg.kv_dim,), Q.F32),
-                              (b + "attn_v.bias", (cfg.kv_dim,), Q.F32)]
-            specs.append((b + "attn_output.weight", (H, cfg.q_dim), wq))
-            if cfg.has_out_bias:
-                specs.append((b + "attn_output.bias", (H,), Q.F32))
-            if cfg.post_norms:
-                specs.append((b + "post_attention_norm.weight", (H,), Q.F32))
-            if cfg.qk_norm:
-                specs += [(b + "attn_q_norm.weight", (cfg.head_dim,), Q.F32),
-                          (b + "attn_k_norm.weight", (cfg.head_dim,), Q.F32)]
-            if cfg.attn_sinks:
-                specs.append((b + "attn_sinks.weight", (cfg.n_heads,), Q.F32))
-        specs.append((b + "ffn_norm.weight", (H,), Q.F32))
-        if cfg.is_moe_layer(i):
-            E, F = cfg.n_experts, cfg.expert_ffn
-            specs += [(b + "ffn_gate_inp.weight", (E, H), Q.F32),
-                      (b + "ffn_gate_exps.weight", (E, F, H), xq),
-                      (b + "ffn_up_exps.weight", (E, F, H), xq),
-                      (b + "ffn_down_exps.weight", (E, H, F), xq)]
-            if cfg.arch == "gpt-oss":
-                specs += [(b + "ffn_gate_inp.bias", (E,), Q.F32),
-                          (b + "ffn_gate_exps.bias", (E, F), Q.F32),
-                          (b + "ffn_up_exps.bias", (E, F), Q.F32),
-                          (b + "ffn_down_exps.bias", (E, H), Q.F32)]
-            if cfg.moe_gating == "sigmoid":
-                specs.append((b + "exp_probs_b.bias", (E,), Q.F32))
-            if cfg.shared_expert_ffn:
-                S = cfg.shared_expert_ffn
-                specs += [(b + "ffn_gate_shexp.weight", (S, H), wq),
-                          (b + "ffn_up_shexp.weight", (S, H), wq),
-                          (b + "ffn_down_shexp.weight", (H, S), wq)]
-                if cfg.shared_expert_gated:
-                    specs.append((b + "ffn_gate_inp_shexp.weight", (H,), Q.F32))
-        elif cfg.fused_gate_up:
-            specs += [(b + "ffn_up.weight", (2 * cfg.ffn, H), wq),
-                      (b + "ffn_down.weight", (H, cfg.ffn), wq)]
-        else:
-            specs += [(b + "ffn_gate.weight", (cfg.ffn, H), wq),
-                      (b + "ffn_up.weight", (cfg.ffn, H), wq),
-                      (b + "ffn_down.weight", (H, cfg.ffn), wq)]
-        if cfg.post_norms and not cfg.is_linear_attn(i):
-            specs.append((b + "post_ffw_norm.weight", (H,), Q.F32))
+        specs += _layer_specs(cfg, i, wq, xq)
+        specs += [(b + "nextn.eh_proj.weight", (H, 2 * H), wq),
+                  (b + "nextn.enorm.weight", (H,), Q.F32),
+                  (b + "nextn.hnorm.weight", (H,), Q.F32),
+                  (b + "nextn.shared_head_norm.weight", (H,), Q.F32)]
     specs.append(("output_norm.weight", (H,), Q.F32))
     if not cfg.tie_embeddings:
         specs.append(("output.weight", (cfg.vocab, H), oq))

@@ -96,3 +96,27 @@ def test_qwen35_metadata_without_engine_keys():
     c = from_gguf_metadata(md)
     assert (c.ssm_k_heads, c.ssm_v_heads, c.ssm_head_dim, c.full_attn_interval) == (2, 4, 128, 4)
     assert c.attn_output_gate and c.qk_norm and c.rope_neox and not c.n_experts
+
+
+@pytest.mark.parametrize("arch", ["qwen35", "gpt-oss"])
+def test_ffn_pre_norm_file_name(arch, tmp_path):
+    """gpt-oss, GLM-4.5 and the Qwen hybrids' files name the norm before the
+    feed-forward post_attention_norm; the engine reads it as ffn_norm."""
+    from swarmllm_b200.gguf.file import GGUFReader
+    from swarmllm_b200.models.config import ModelConfig
+    from swarmllm_b200.models.weights import GgufSource, RandomSource, write_random_gguf
+    if arch == "gpt-oss":
+        cfg = ModelConfig(name="t-oss", arch="gpt-oss", n_layers=2, hidden=256, n_heads=8,
+                          n_kv_heads=2, head_dim=64, ffn=128, vocab=512, attn_bias=True,
+                          attn_sinks=True, sliding_window=16, swa_every=2, n_experts=4,
+                          n_experts_used=2, expert_ffn=128, swiglu_limit=7.0,
+                          weight_qtype="Q8_0", embed_qtype="Q8_0", output_qtype="Q8_0",
+                          expert_qtype="MXFP4")
+    else:
+        cfg = _cfg("qwen35", "Q8_0", False)
+    path = write_random_gguf(cfg, str(tmp_path / "m.gguf"), seed=2)
+    names = set(GGUFReader(path).tensors)
+    assert "blk.0.post_attention_norm.weight" in names and "blk.0.ffn_norm.weight" not in names
+    a, _, _ = GgufSource(path).get("blk.1.ffn_norm.weight")
+    b, _, _ = RandomSource(cfg, seed=2).get("blk.1.ffn_norm.weight")
+    assert torch.equal(a, b)
