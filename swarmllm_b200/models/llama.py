@@ -661,7 +661,10 @@ class LlamaCPU:
     prefill_attn.rs and fast_math.rs."""
 
     def __init__(self, cfg: ModelConfig, source, layer_range: tuple[int, int] | None = None,
-                 kv_layer_offset: int | None = None, dtype=torch.float32, native: bool = False):
+                 kv_layer_offset: int | None = None, dtype=torch.float32, native: bool = False,
+                 mtp: bool = False):
+        """mtp: also load the file's next-token-prediction block (the last
+        stage of a model with `mtp_layers`), for `mtp_forward`."""
         self.cfg = cfg
         lo, hi = layer_range or (0, cfg.n_layers)
         self.lo, self.hi = lo, hi
@@ -715,6 +718,22 @@ class LlamaCPU:
         if self.last:
             self.out_norm = dq("output_norm.weight")
             self.head = lw("token_embd.weight" if cfg.tie_embeddings else "output.weight")
+        self.mtp = None
+        if mtp and cfg.mtp_layers and self.last:
+            if not self.first:
+                raise ValueError("the next-token-prediction block needs the token table")
+            i = cfg.n_layers
+            b = f"blk.{i}."
+            M = _GpuLayer()
+            M.attn_norm, M.ffn_norm = dq(b + "attn_norm.weight"), dq(b + "ffn_norm.weight")
+            M.linear = False
+            self._load_attn(M, i, b, dq, lw)
+            self._load_ffn_cpu(M, b, dq, lw)
+            M.eh_proj = lw(b + "nextn.eh_proj.weight")
+            M.enorm, M.hnorm = dq(b + "nextn.enorm.weight"), dq(b + "nextn.hnorm.weight")
+            hn = b + "nextn.shared_head_norm.weight"
+            M.head_norm = dq(hn) if source.has(hn) else self.out_norm
+            self.mtp = M
         inv, self.attn_factor = rope_inv_freq(cfg)
         self.inv_freq = torch.from_numpy(inv)
         inv_l, self.attn_factor_local = rope_inv_freq(cfg, local=True)
@@ -1011,6 +1030,26 @@ class LlamaCPU:
         if want_hidden:
             return logits, self._norm(h, self.out_norm)
         return logits
+
+    def mtp_forward(self, tokens: torch.Tensor, hidden: torch.Tensor, b: StepBatch,
+                    kv: PagedKVCache):
+        """The next-token-prediction block: row r pairs token tokens[r] (the
+        token at position b.positions[r]) with `hidden[r]`, the output-normed
+        trunk state at the position before it, and predicts the token after:
+        eh_proj([enorm(embedding) | hnorm(hidden)]) -> one full-attention layer
+        over its own one-layer cache `kv` -> head norm -> the output head.
+        Returns (logits of b.sample_rows, head-normed state of every row, which
+        the next draft step reads as its hidden state).  As llama.cpp's
+        qwen35 graph_mtp / the reference's split/mtp.rs lay it out."""
+        M = self.mtp
+        e = self._norm(self.embd[tokens.long()].to(self.dtype), M.enorm)
+        x_res = self._mm(torch.cat([e, self._norm(hidden.to(self.dtype), M.hnorm)], -1), M.eh_proj)
+        ps = kv.page_size
+        slots = b.slots.long()
+        h = self._attn_layer(M, self.cfg.n_layers, x_res, self._norm(x_res, M.attn_norm), b, kv, 0,
+                             slots // ps, slots % ps)
+        out = self._norm(h, M.head_norm)
+        return self._logits(out[b.sample_rows.long()]), out
 
     def _logits(self, x):
         logits = self._mm(x, self.head)
