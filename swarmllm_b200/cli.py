@@ -87,6 +87,28 @@ def _engine(args):
     return eng
 
 
+def _mtp_generate(eng, tok, ids, args) -> dict:
+    """Greedy generation through the MTP speculator (CPU model)."""
+    from .engine.mtp import MtpSpeculator
+    from .models.llama import LlamaCPU
+    if eng.cfg.mtp_layers < 1 or not isinstance(eng.model, LlamaCPU):
+        raise SystemExit("--mtp-depth needs a model with a next-token-prediction block, on the CPU")
+    m = eng.model
+    if m.mtp is None:
+        src = getattr(eng, "source", None)
+        if src is None:
+            from .models.weights import GgufSource, RandomSource
+            src = GgufSource(args.gguf) if args.gguf else RandomSource(eng.cfg, seed=args.seed)
+        m = LlamaCPU(eng.cfg, src, native=m.native, mtp=True)
+    spec = MtpSpeculator(m, depth=args.mtp_depth,
+                         max_len=len(ids) + args.max_tokens + args.mtp_depth + 16)
+    toks = spec.generate(ids, args.max_tokens)
+    st = spec.stats
+    return {"token_ids": toks, "text": tok.decode(toks), "mtp_rounds": st.rounds,
+            "mtp_acceptance": round(st.acceptance, 4),
+            "tokens_per_round": round(st.tokens_per_round, 3)}
+
+
 def _tokenizer(args, eng):
     from .serve.tokenizer import ByteTokenizer, from_gguf_metadata
     if args.gguf:
@@ -183,6 +205,9 @@ def main(argv=None):
             s.add_argument("--max-tokens", type=int, default=32)
             s.add_argument("--temperature", type=float, default=0.0)
             s.add_argument("--adapter", default=None, help="name of a --lora adapter to generate with")
+            s.add_argument("--mtp-depth", type=int, default=0,
+                           help="CPU, greedy: draft this many tokens a round with the model's own "
+                                "next-token-prediction block and verify them with the trunk")
         if name == "chat":
             s.add_argument("--max-tokens", type=int, default=256)
             s.add_argument("--temperature", type=float, default=0.7)
@@ -275,6 +300,9 @@ def main(argv=None):
     if args.cmd == "generate":
         tok, _ = _tokenizer(args, eng)
         ids = [int(x) for x in args.ids.split(",")] if args.ids else tok.encode(args.prompt)
+        if args.mtp_depth:
+            print(json.dumps(_mtp_generate(eng, tok, ids, args)))
+            return
         sp = SamplingParams(max_tokens=args.max_tokens, temperature=args.temperature)
         rid = eng.add_request(ids, sp, lora=args.adapter) if args.adapter else eng.add_request(ids, sp)
         toks = []

@@ -113,3 +113,17 @@ def test_accepted_chains_commit_several_tokens(make, monkeypatch):
     st = spec.stats
     # round 1 keeps the two tokens before the wrong one; the rest are all kept
     assert st.drafted - st.accepted == 2 and st.tokens_per_round > 2.0
+
+
+def test_cli_generate_with_mtp(tmp_path, capsys):
+    import json
+
+    from swarmllm_b200.cli import main
+    from swarmllm_b200.models.weights import write_random_gguf
+    path = write_random_gguf(_dense(), str(tmp_path / "m.gguf"), seed=2)
+    main(["generate", "--gguf", path, "--device", "cpu", "--ids", "5,6,7,8", "--max-tokens", "6"])
+    plain = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    main(["generate", "--gguf", path, "--device", "cpu", "--ids", "5,6,7,8", "--max-tokens", "6",
+          "--mtp-depth", "3"])
+    spec = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert spec["token_ids"] == plain["token_ids"] and spec["mtp_rounds"] >= 1
