@@ -88,12 +88,24 @@ def _engine(args):
 
 
 def _mtp_generate(eng, tok, ids, args) -> dict:
-    """Greedy generation through the MTP speculator (CPU model)."""
+    """Greedy generation through the MTP or block-drafter speculator (CPU model)."""
     from .engine.mtp import MtpSpeculator
     from .models.llama import LlamaCPU
-    if eng.cfg.mtp_layers < 1 or not isinstance(eng.model, LlamaCPU):
-        raise SystemExit("--mtp-depth needs a model with a next-token-prediction block, on the CPU")
+    if not isinstance(eng.model, LlamaCPU):
+        raise SystemExit("--mtp-depth / --block-drafter run on the CPU model (--device cpu)")
     m = eng.model
+    if args.block_drafter:
+        from .engine.block_spec import BlockSpeculator
+        from .models.dflash import DFlashDrafter
+        d = DFlashDrafter(args.block_drafter, m)
+        spec = BlockSpeculator(m, d, max_len=len(ids) + args.max_tokens + d.cfg.block_size + 16)
+        toks = spec.generate(ids, args.max_tokens)
+        st = spec.stats
+        return {"token_ids": toks, "text": tok.decode(toks), "rounds": st.rounds,
+                "acceptance": round(st.acceptance, 4),
+                "tokens_per_round": round(st.tokens_per_round, 3)}
+    if eng.cfg.mtp_layers < 1:
+        raise SystemExit("--mtp-depth needs a model with a next-token-prediction block")
     if m.mtp is None:
         src = getattr(eng, "source", None)
         if src is None:
@@ -205,6 +217,9 @@ def main(argv=None):
             s.add_argument("--max-tokens", type=int, default=32)
             s.add_argument("--temperature", type=float, default=0.0)
             s.add_argument("--adapter", default=None, help="name of a --lora adapter to generate with")
+            s.add_argument("--block-drafter", default=None,
+                           help="CPU, greedy: a DFlash block drafter GGUF guessing a block a round, "
+                                "verified by the model")
             s.add_argument("--mtp-depth", type=int, default=0,
                            help="CPU, greedy: draft this many tokens a round with the model's own "
                                 "next-token-prediction block and verify them with the trunk")
@@ -300,7 +315,7 @@ def main(argv=None):
     if args.cmd == "generate":
         tok, _ = _tokenizer(args, eng)
         ids = [int(x) for x in args.ids.split(",")] if args.ids else tok.encode(args.prompt)
-        if args.mtp_depth:
+        if args.mtp_depth or args.block_drafter:
             print(json.dumps(_mtp_generate(eng, tok, ids, args)))
             return
         sp = SamplingParams(max_tokens=args.max_tokens, temperature=args.temperature)

@@ -28,60 +28,23 @@ src/inference/model_worker.rs.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
-
 import torch
 
-from ..models.llama import StepBatch
 from ..ops.attention import PagedKVCache
+from .chain_spec import ChainSpec, SpecStats
+
+MtpStats = SpecStats
 
 
-@dataclass
-class MtpStats:
-    rounds: int = 0
-    drafted: int = 0
-    accepted: int = 0
-
-    @property
-    def acceptance(self) -> float:
-        return self.accepted / self.drafted if self.drafted else 0.0
-
-    @property
-    def tokens_per_round(self) -> float:
-        return (self.accepted + self.rounds) / self.rounds if self.rounds else 0.0
-
-
-class MtpSpeculator:
+class MtpSpeculator(ChainSpec):
     def __init__(self, model, depth: int = 3, max_len: int = 2048, page_size: int = 16):
         if model.mtp is None:
             raise ValueError("the model was loaded without its next-token-prediction block")
-        self.m, self.depth = model, depth
+        super().__init__(model, max_len, page_size)
+        self.depth = depth
         cfg = model.cfg
-        self.ps = page_size
-        self.pages = (max_len + page_size - 1) // page_size + 1
-        self.max_len = max_len
-        self.kv = PagedKVCache(model.n_kv_layers, self.pages, cfg.n_kv_heads, cfg.head_dim, "cpu",
-                               page_size, dtype=torch.float32)
-        spec = model.linear_state_spec()
-        if spec:
-            self.kv.add_linear_state(spec[0], 1, *spec[1:])
         self.kv_mtp = PagedKVCache(1, self.pages, cfg.n_kv_heads, cfg.head_dim, "cpu", page_size,
                                    dtype=torch.float32)
-        self.bt = torch.arange(self.pages, dtype=torch.int32)
-        self.stats = MtpStats()
-
-    # ------------------------------------------------------------------ batches
-    def _batch(self, tokens, p0: int, sample_all: bool = True) -> StepBatch:
-        n = len(tokens)
-        pos = torch.arange(p0, p0 + n, dtype=torch.int32)
-        ssm = torch.tensor([[0, n, 0, p0]], dtype=torch.int32) if self.m.n_lin_layers else None
-        rows = torch.arange(n) if sample_all else torch.tensor([n - 1])
-        return StepBatch(torch.as_tensor(tokens, dtype=torch.int32), pos, pos,
-                         self.bt.repeat(n, 1), pos + 1, rows, p0 + n, ssm_seqs=ssm)
-
-    def _trunk(self, tokens, p0):
-        logits, hidden = self.m.forward(self._batch(tokens, p0), self.kv, want_hidden=True)
-        return logits, hidden
 
     def _head(self, tokens, hidden, p0):
         return self.m.mtp_forward(torch.as_tensor(tokens, dtype=torch.int32), hidden,
@@ -101,17 +64,6 @@ class MtpSpeculator:
             d.append(int(lg[-1].argmax()))
         return d
 
-    def _save_state(self):
-        if self.kv.ssm is None:
-            return None
-        return self.kv.ssm.clone(), self.kv.conv.clone()
-
-    def _restore_state(self, st):
-        if st is not None:
-            self.kv.ssm.copy_(st[0])
-            self.kv.conv.copy_(st[1])
-
-    # ------------------------------------------------------------------ decoding
     def generate(self, prompt: list[int], max_new: int) -> list[int]:
         """Greedy continuation of `prompt` (max_new tokens)."""
         n = len(prompt)
@@ -122,30 +74,16 @@ class MtpSpeculator:
         out = [y]
         # the head over the prompt: position p pairs x_p with h_{p-1}; the last
         # row pairs the new token y with the last prompt state
-        toks = list(prompt[1:]) + [y]
-        lg, hout = self._head(toks, hidden, 1)
+        lg, hout = self._head(list(prompt[1:]) + [y], hidden, 1)
         draft = self._draft(lg, hout, n + 1)
         pos = n                          # position of y, the last committed token
         while len(out) < max_new:
-            draft = draft[: max_new - len(out)]
-            st = self._save_state()
-            vlog, vhid = self._trunk([y] + draft, pos)
-            a = 0
-            while a < len(draft) and int(vlog[a].argmax()) == draft[a]:
-                a += 1
-            bonus = int(vlog[a].argmax())
-            self.stats.rounds += 1
-            self.stats.drafted += len(draft)
-            self.stats.accepted += a
-            if a < len(draft) and st is not None:
-                # the recurrent state ran over rejected rows: rerun the kept ones
-                self._restore_state(st)
-                self._trunk([y] + draft[:a], pos)
+            a, bonus, vhid = self._check(y, draft[: max_new - len(out)], pos)
             new = draft[:a] + [bonus]
             out += new
             # the head's cache: the committed positions pos+1 .. pos+a+1, each
             # paired with the trunk's state one position earlier
-            lg, hout = self._head(new, vhid[: a + 1], pos + 1)
+            lg, hout = self._head(new, vhid, pos + 1)
             pos += a + 1
             y = bonus
             if len(out) < max_new:

@@ -1002,11 +1002,15 @@ class LlamaCPU:
         return y
 
     def forward(self, b: StepBatch, kv: PagedKVCache, ctx=None, h_in=None,
-                want_hidden: bool = False) -> torch.Tensor:
+                want_hidden: bool = False, capture=()) -> torch.Tensor:
         """Logits of the sample rows (the last stage), or the residual stream
         (other stages).  want_hidden: also the output-normed hidden state of
-        every row, (logits, hidden) -- what a next-token-prediction head reads."""
+        every row, (logits, hidden) -- what a next-token-prediction head reads.
+        capture: absolute layer indices whose INPUT residual stream (every row)
+        is kept in self.captured[layer] (n_layers: the stream after the last
+        layer) -- what a block drafter reads."""
         cfg = self.cfg
+        self.captured = {}
         h = self.embd[b.tokens.long()].clone() if self.first else h_in.to(self.dtype).clone()
         if self.first and cfg.embed_scale:
             h = h * cfg.embed_scale
@@ -1016,6 +1020,8 @@ class LlamaCPU:
         slots = b.slots.long()
         pages, offs = slots // ps, slots % ps
         for j, L in enumerate(self.layers):
+            if self.lo + j in capture:
+                self.captured[self.lo + j] = h.clone()
             x = self._norm(h, L.attn_norm)
             if L.linear:
                 h = h + self._deltanet(L, x, b, kv)
@@ -1023,6 +1029,8 @@ class LlamaCPU:
                 h = h + self._ffn(L, x)
                 continue
             h = self._attn_layer(L, self.lo + j, h, x, b, kv, self.kv_off + L.kv_idx, pages, offs)
+        if self.hi in capture:
+            self.captured[self.hi] = h.clone()
         if not self.last:
             return h
         x = self._norm(h[b.sample_rows.long()], self.out_norm)
