@@ -45,6 +45,17 @@ GGUF architecture name (llama.cpp's names and metadata keys):
                 scaled, plus an ungated shared expert; the file's
                 ``post_attention_norm`` is the norm before the FFN; the
                 trailing next-token-prediction blocks are not run.
+* ``llama4``    Llama 4 (Scout / Maverick): interleaved RoPE with every 4th
+                layer NoPE, per-head q/k RMS normalisation without a weight
+                on the RoPE layers, sigmoid-scored experts whose weight
+                scales the expert's input, an ungated shared expert, dense
+                and routed layers interleaved (``interleave_moe_layer_step``).
+                Runs on the CPU model; the GPU model refuses it by name.
+* ``granite``   Llama with four multipliers (embedding, residual, attention,
+                logit).  The GPU model runs files whose residual multiplier is
+                1 (the others map to options it has); the CPU model runs all.
+* ``qwen2vl`` / ``qwen3vl`` files: their text trunk is read as ``qwen2`` /
+  ``qwen3``.
 """
 from __future__ import annotations
 
@@ -99,6 +110,13 @@ class ModelConfig:
     moe_norm_topk: bool = True          # sigmoid gating: weights divided by their sum
     moe_scale: float = 1.0              # sigmoid gating: routed-weight multiplier
     moe_dense_layers: int = 0           # leading layers with a dense FFN (size `ffn`)
+    moe_every: int = 0                  # > 1: only every Nth layer (1-based) routes (llama4 interleave)
+    moe_sel_bias: bool = True           # sigmoid gating: the file has an exp_probs_b selection bias
+    moe_weight_input: bool = False      # routed weight scales the expert's input, not its output (llama4)
+    nope_every: int = 0                 # every Nth layer (1-based) has no RoPE (llama4 iRoPE)
+    qk_rms_plain: bool = False          # q/k RMS-normalised per head without a weight on RoPE layers (llama4)
+    residual_scale: float = 0.0         # branch outputs times this before the residual add (granite; 0: none)
+    logit_scale: float = 0.0            # output logits divided by this (granite; 0: none)
     shared_expert_gated: bool = True    # a sigmoid gate (ffn_gate_inp_shexp) on the shared expert
     mtp_layers: int = 0                 # next-token-prediction blocks after the trunk (blk.{n_layers})
     swiglu_limit: float = 0.0           # gpt-oss clamped SwiGLU (7.0)
@@ -163,7 +181,13 @@ class ModelConfig:
         return None
 
     def is_moe_layer(self, layer: int) -> bool:
-        return bool(self.n_experts) and layer >= self.moe_dense_layers
+        if not self.n_experts or layer < self.moe_dense_layers:
+            return False
+        return self.moe_every <= 1 or (layer + 1) % self.moe_every == 0
+
+    def is_nope(self, layer: int) -> bool:
+        """A layer without rotary position embedding (llama4: every 4th)."""
+        return bool(self.nope_every) and (layer + 1) % self.nope_every == 0
 
     @property
     def moe_mode(self) -> int:
@@ -345,14 +369,22 @@ def preset(name: str) -> ModelConfig:
 
 # --------------------------------------------------------------------------- GGUF mapping
 _FAMILIES = ("llama", "mistral", "qwen2", "qwen3", "qwen2moe", "qwen3moe", "gemma", "gemma2",
-             "gemma3", "phi3", "glm4", "glm4moe", "gpt-oss", "qwen3next", "qwen35", "qwen35moe")
+             "gemma3", "phi3", "glm4", "glm4moe", "gpt-oss", "qwen3next", "qwen35", "qwen35moe",
+             "llama4", "granite")
 _ARCH_KEYS = {f: f for f in _FAMILIES}    # GGUF general.architecture == family name
+# Architecture names whose language model is another family's, tensor for
+# tensor: the Qwen2.5-VL / Qwen3-VL text trunks (their multimodal position
+# sections turn a text-only position as NEOX RoPE does; image inputs are the
+# vision encoder's business).  Reference: src/inference/model_arch.rs:84-99.
+_ARCH_ALIASES = {"qwen2vl": "qwen2", "qwen3vl": "qwen3"}
 
 
-def apply_family(cfg: ModelConfig, md: dict | None = None) -> ModelConfig:
-    """Set the options a family implies (and those its GGUF metadata carries)."""
+def apply_family(cfg: ModelConfig, md: dict | None = None, prefix: str | None = None) -> ModelConfig:
+    """Set the options a family implies (and those its GGUF metadata carries,
+    under the keys of `prefix`, the file's architecture name)."""
     fam = cfg.arch
-    g = (lambda k, d=None: md.get(f"{fam}.{k}", d)) if md is not None else (lambda k, d=None: d)
+    pre = prefix or fam
+    g = (lambda k, d=None: md.get(f"{pre}.{k}", d)) if md is not None else (lambda k, d=None: d)
     if fam in ("qwen2", "qwen2moe"):
         cfg.rope_neox, cfg.attn_bias, cfg.attn_out_bias = True, True, False
     if fam in ("qwen3", "qwen3moe"):
@@ -393,6 +425,33 @@ def apply_family(cfg: ModelConfig, md: dict | None = None) -> ModelConfig:
         cfg.swiglu_limit = cfg.swiglu_limit or 7.0
     if fam in ("qwen3next", "qwen35", "qwen35moe"):
         cfg.rope_neox, cfg.qk_norm, cfg.attn_output_gate = True, True, True
+    if fam == "llama4":
+        # iRoPE: every 4th layer has no rotary embedding; the RoPE layers
+        # normalise q and k per head by their RMS with no weight (not in the
+        # 128-expert Maverick); experts scored by a sigmoid, no selection bias,
+        # no renormalisation, the weight applied to the expert's input, an
+        # ungated shared expert; dense and routed layers interleaved.
+        # Reference: src/inference/split/loader/mod.rs:1346 (routing),
+        # :2392 (NoPE layers, q/k norm after RoPE).
+        cfg.rope_neox, cfg.nope_every = False, 4
+        cfg.qk_rms_plain = cfg.n_experts != 128
+        if cfg.n_experts:
+            cfg.moe_gating, cfg.moe_norm_topk, cfg.moe_scale = "sigmoid", False, 1.0
+            cfg.moe_sel_bias, cfg.moe_weight_input, cfg.shared_expert_gated = False, True, False
+            cfg.moe_every = int(g("interleave_moe_layer_step", cfg.moe_every or 1))
+            if md is not None and not cfg.shared_expert_ffn:
+                cfg.shared_expert_ffn = cfg.expert_ffn
+    if fam == "granite" and md is not None:
+        # Llama read with four multipliers (llama.cpp's granite keys; 0 or 1
+        # means none for the embedding and residual ones); the attention
+        # multiplier is the generic attention.scale.  Reference:
+        # src/inference/model_arch.rs:77-81, split/gguf_meta.rs:594.
+        emb = float(g("embedding_scale", 0.0) or 0.0)
+        cfg.embed_scale = emb if emb not in (0.0, 1.0) else cfg.embed_scale
+        res = float(g("residual_scale", 0.0) or 0.0)
+        cfg.residual_scale = res if res not in (0.0, 1.0) else 0.0
+        lg = float(g("logit_scale", 0.0) or 0.0)
+        cfg.logit_scale = lg if lg not in (0.0, 1.0) else 0.0
     if fam in ("qwen35", "qwen35moe") and md is not None:
         # Qwen 3.5 files count only the trunk in block_count; the block after it
         # (blk.{block_count}) is the next-token-prediction head
@@ -437,6 +496,14 @@ def to_gguf_metadata(cfg: ModelConfig) -> dict:
             md[f"{a}.leading_dense_block_count"] = cfg.moe_dense_layers
     if cfg.mtp_layers:
         md[f"{a}.nextn_predict_layers"] = cfg.mtp_layers
+    if cfg.arch == "llama4" and cfg.moe_every > 1:
+        md[f"{a}.interleave_moe_layer_step"] = cfg.moe_every
+    if cfg.arch == "granite":
+        for key, v in (("embedding_scale", cfg.embed_scale), ("residual_scale", cfg.residual_scale),
+                       ("logit_scale", cfg.logit_scale)):
+            md[f"{a}.{key}"] = float(v or 1.0)
+    if cfg.attn_scale:
+        md[f"{a}.attention.scale"] = float(cfg.attn_scale)
     if cfg.sliding_window:
         md[f"{a}.attention.sliding_window"] = cfg.sliding_window
     if cfg.attn_softcap:
@@ -460,7 +527,7 @@ def from_gguf_metadata(md: dict) -> ModelConfig:
     if "swarmllm.config" in md:
         return ModelConfig(**json.loads(md["swarmllm.config"]))
     arch = md["general.architecture"]
-    fam = arch if arch in _FAMILIES else None
+    fam = arch if arch in _FAMILIES else _ARCH_ALIASES.get(arch)
     if fam is None:
         raise ValueError(f"unsupported architecture {arch}")
     a = arch
@@ -505,4 +572,4 @@ def from_gguf_metadata(md: dict) -> ModelConfig:
             raise ValueError("DeltaNet value heads wider than key heads are not supported")
     if fam in ("gemma", "gemma2", "gemma3") and not g("vocab_size"):
         cfg.vocab = len(md.get("tokenizer.ggml.tokens", [])) or cfg.vocab
-    return apply_family(cfg, md)
+    return apply_family(cfg, md, prefix=a)

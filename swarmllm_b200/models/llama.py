@@ -74,6 +74,14 @@ class LlamaGPU:
         -- this rank holds n_heads/W query heads, n_kv/W KV heads and ffn/W
         FFN features; o_proj/down_proj partials are summed over the group by
         the GEMM epilogues."""
+        unbuilt = [what for what, on in (
+            ("layers without RoPE (llama4 iRoPE)", cfg.nope_every),
+            ("q/k RMS normalisation without a weight (llama4)", cfg.qk_rms_plain),
+            ("experts weighted on their input (llama4)", cfg.moe_weight_input),
+            ("a residual multiplier (granite)", cfg.residual_scale)) if on]
+        if unbuilt:
+            raise NotImplementedError(f"{cfg.arch} on the GPU model: {', '.join(unbuilt)} not "
+                                      "built in the kernels; the CPU model (device='cpu') runs it")
         self.cfg = cfg
         self.ep = ep
         self.tp = tp
@@ -281,7 +289,8 @@ class LlamaGPU:
         t, rq, _ = get(b + "ffn_gate_inp.weight")
         L.router = QLinear(t, rq, E, H, dev, f32_as_f16=True)
         L.router_b = small(b + "ffn_gate_inp.bias") if cfg.arch == "gpt-oss" else None
-        L.sel_b = small(b + "exp_probs_b.bias") if cfg.moe_gating == "sigmoid" else None
+        L.sel_b = (small(b + "exp_probs_b.bias") if cfg.moe_gating == "sigmoid" and cfg.moe_sel_bias
+                   else None)
         L.sh_gu = L.sh_down = L.sh_gate = None
         if cfg.shared_expert_ffn:
             W, tr = (self.tp.world, self.tp.rank) if self.tp else (1, 0)
@@ -512,6 +521,8 @@ class LlamaGPU:
             C().epi_copy(g, None, logits)
             if cfg.final_softcap:  # c * tanh(logits / c)
                 logits.div_(cfg.final_softcap).tanh_().mul_(cfg.final_softcap)
+            if cfg.logit_scale:  # granite: logits divided by its multiplier
+                logits.div_(cfg.logit_scale)
         return logits
 
     def _stage_ctx(self):
@@ -782,7 +793,8 @@ class LlamaCPU:
             L.ebg = dq(b + "ffn_gate_exps.bias") if gpt else None
             L.ebu = dq(b + "ffn_up_exps.bias") if gpt else None
             L.ebd = dq(b + "ffn_down_exps.bias") if gpt else None
-            L.sel_b = dq(b + "exp_probs_b.bias") if cfg.moe_gating == "sigmoid" else None
+            L.sel_b = (dq(b + "exp_probs_b.bias") if cfg.moe_gating == "sigmoid" and cfg.moe_sel_bias
+                       else None)
             L.sg = L.sgi = None
             if cfg.shared_expert_ffn:
                 L.sg, L.su, L.sd = (lw(b + n) for n in ("ffn_gate_shexp.weight", "ffn_up_shexp.weight",
@@ -991,6 +1003,8 @@ class LlamaCPU:
             rows = sel.any(1).nonzero().flatten()
             we = (w * sel).sum(1)[rows]
             xs = x[rows]
+            if cfg.moe_weight_input:  # llama4: the expert sees its weight times the input
+                xs, we = xs * we[:, None], torch.ones_like(we)
             mm, ex = self._mm, self._expert
             g = mm(xs, ex(L.eg, e)) + (L.ebg[e] if L.ebg is not None else 0)
             u = mm(xs, ex(L.eu, e)) + (L.ebu[e] if L.ebu is not None else 0)
@@ -1063,6 +1077,8 @@ class LlamaCPU:
         logits = self._mm(x, self.head)
         if self.cfg.final_softcap:
             logits = self.cfg.final_softcap * torch.tanh(logits / self.cfg.final_softcap)
+        if self.cfg.logit_scale:
+            logits = logits / self.cfg.logit_scale
         return logits
 
     def _attn_layer(self, L, layer, h, x, b, kv, li, pages, offs):
@@ -1084,7 +1100,12 @@ class LlamaCPU:
         q, k, v = q.reshape(N, nq, d), k.view(N, nkv, d), v.view(N, nkv, d)
         if L.q_norm is not None:
             q, k = self._norm(q, L.q_norm), self._norm(k, L.k_norm)
-        q, k = self._rope(q, b.positions, L.local_rope), self._rope(k, b.positions, L.local_rope)
+        if not cfg.is_nope(layer):
+            if cfg.qk_rms_plain:
+                # llama4 normalises after RoPE; a rotation keeps every pair's
+                # length, so the head's RMS (and this result) is the same
+                q, k = self._norm(q, 1.0), self._norm(k, 1.0)
+            q, k = self._rope(q, b.positions, L.local_rope), self._rope(k, b.positions, L.local_rope)
         K, V = kv.k(li), kv.v(li)
         K[pages, :, offs, :] = k.to(K.dtype)
         V[pages, :, offs, :] = v.to(V.dtype)
@@ -1100,12 +1121,13 @@ class LlamaCPU:
             o = o + L.bo
         if L.post_attn is not None:
             o = self._norm(o, L.post_attn)
-        h = h + o
+        rs = cfg.residual_scale or 1.0
+        h = h + o * rs
         x = self._norm(h, L.ffn_norm)
         f = self._ffn(L, x, layer, b)
         if L.post_ffn is not None:
             f = self._norm(f, L.post_ffn)
-        return h + f
+        return h + f * rs
 
     def _attention(self, L, q, K, V, b):
         """The fp32 oracle: per row, gather its keys and take a plain softmax."""

@@ -77,7 +77,7 @@ def _layer_specs(cfg: ModelConfig, i: int, wq: int, xq: int) -> list:
                       (b + "ffn_gate_exps.bias", (E, F), Q.F32),
                       (b + "ffn_up_exps.bias", (E, F), Q.F32),
                       (b + "ffn_down_exps.bias", (E, H), Q.F32)]
-        if cfg.moe_gating == "sigmoid":
+        if cfg.moe_gating == "sigmoid" and cfg.moe_sel_bias:
             specs.append((b + "exp_probs_b.bias", (E,), Q.F32))
         if cfg.shared_expert_ffn:
             S = cfg.shared_expert_ffn
