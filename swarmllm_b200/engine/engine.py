@@ -390,27 +390,17 @@ class LLMEngine:
         self.steps += 1
         return out
 
-    CONSTRAINT_CANDIDATES = 64
-
     def _constrain(self, params, sampled):
         """Apply per-request token constraints to the sampled rows: keep the
         drawn token if allowed, else the best allowed candidate by logit (the
         top 64, then the whole row).  Runs before the scheduler commits."""
+        from .sampling import constrained_token
         sampled = np.array(sampled, copy=True)
         logits = self.runner.last_logits
         for k, p in enumerate(params):
-            c = p.constraint
-            if c is None:
-                continue
-            row = logits[k].float()
-            top = torch.topk(row, min(self.CONSTRAINT_CANDIDATES, row.numel())).indices.tolist()
-            t = c.choose(int(sampled[k]), top)
-            if t is None:
-                t = c.choose(int(sampled[k]), torch.argsort(row, descending=True).tolist())
-            if t is None:   # nothing keeps the text valid: end the reply
-                t = p.eos_token_id if p.eos_token_id >= 0 else int(sampled[k])
-            c.accept(t)
-            sampled[k] = t
+            if p.constraint is not None:
+                sampled[k] = constrained_token(p.constraint, int(sampled[k]), logits[k],
+                                               p.eos_token_id)
         return sampled
 
     def embed_text(self, ids: list[int]) -> list[float]:

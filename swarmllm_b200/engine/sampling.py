@@ -169,3 +169,24 @@ def sample_host(logits: torch.Tensor, params: list[SamplingParams], positions,
         g = -np.log(-np.log(u))
         out[r] = int(np.argmax(np.where(keep, z + g, -np.inf)))
     return out
+
+
+# allowed-token search of a constrained reply: the top logits first, then the row
+CONSTRAINT_CANDIDATES = 64
+
+
+def constrained_token(c, drawn: int, row, eos: int) -> int:
+    """The token a constrained reply commits at one position: the drawn token
+    if the constraint allows it, else the best allowed candidate by logit
+    (the top 64, then the whole row); end of sequence when nothing keeps the
+    text valid.  The constraint is told the token (c.accept)."""
+    import torch
+    row = row.float()
+    top = torch.topk(row, min(CONSTRAINT_CANDIDATES, row.numel())).indices.tolist()
+    t = c.choose(int(drawn), top)
+    if t is None:
+        t = c.choose(int(drawn), torch.argsort(row, descending=True).tolist())
+    if t is None:
+        t = eos if eos >= 0 else int(drawn)
+    c.accept(t)
+    return int(t)

@@ -145,7 +145,35 @@ class _Side:
         self.bm.truncate(sid, root + keep)
 
 
+def walk_constrained(tree, target: list, logits, params: SamplingParams):
+    """The verify walk of a constrained reply (JSON / schema): at each node on
+    the path the committed token is what plain constrained decoding commits
+    there -- the target's token if the constraint allows it, else the best
+    allowed candidate of that node's logits -- and the walk follows the child
+    carrying it.  Every committed token (path nodes and the bonus) is told to
+    the constraint once, in order, so the reply equals plain constrained
+    decoding.  Reference: src/inference/reply_grammar.rs:334
+    (guesses_it_allows: a check carries only the guesses the grammar allows)."""
+    from .sampling import constrained_token
+    parents, toks = tree.parents(), tree.tokens()
+    child = {}
+    for i in range(1, len(toks)):
+        child.setdefault((parents[i], toks[i]), i)   # first match, as DraftTree.walk
+    path, cur = [0], 0
+    while True:
+        t = constrained_token(params.constraint, int(target[cur]), logits[cur],
+                              params.eos_token_id)
+        nxt = child.get((cur, t))
+        if nxt is None:
+            return path, t
+        path.append(nxt)
+        cur = nxt
+
+
 class TreeSpecDecoder:
+    # constrained replies are verified by walk_constrained
+    constrained = True
+
     def __init__(self, target, drafter, depth: int = 4, width: int = 4, max_seqs: int = 32,
                  max_model_len: int = 4096, prefill_chunk: int = 2048):
         assert 1 + depth * width <= 64, "tree masks are 64-bit: at most 64 nodes"
@@ -195,6 +223,9 @@ class TreeSpecDecoder:
         lg = self._prefill(self.t, sid, prompt)
         self._prefill(self.d, sid, prompt)
         s.root = int(self.t_sampler.sample(lg[:1], [s.params], [len(prompt) - 1])[0])
+        if s.params.constraint is not None:
+            from .sampling import constrained_token
+            s.root = constrained_token(s.params.constraint, s.root, lg[0], s.params.eos_token_id)
         s.commit([s.root])
         s.pos = s.dpos = len(prompt)
         return s
@@ -282,7 +313,11 @@ class TreeSpecDecoder:
         for s in seqs:
             tr = trees[s.sid]
             n = len(tr)
-            path, bonus = tr.walk(tgt[k0:k0 + n].tolist())
+            if s.params.constraint is not None:
+                path, bonus = walk_constrained(tr, tgt[k0:k0 + n].tolist(), logits[k0:k0 + n],
+                                               s.params)
+            else:
+                path, bonus = tr.walk(tgt[k0:k0 + n].tolist())
             k0 += n
             toks = tr.tokens()
             new = [toks[i] for i in path[1:]] + [bonus]

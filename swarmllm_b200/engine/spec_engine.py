@@ -30,6 +30,7 @@ mirrors for the tree depth.
 from __future__ import annotations
 
 import collections
+import dataclasses
 import itertools
 import time
 
@@ -163,8 +164,10 @@ class SpecEngine:
         if lora is not None or images:
             raise ValueError("the speculative engine serves base-model text requests")
         params = params or SamplingParams()
-        if params.penalized or params.constraint is not None:
-            raise ValueError("penalties, logit bias and constraints are not served speculatively")
+        if params.penalized:
+            raise ValueError("penalties and logit bias are not served speculatively")
+        if params.constraint is not None and not getattr(self.dec, "constrained", False):
+            raise ValueError("constrained replies are served by the draft-tree speculator only")
         rid = next(self._ids) if request_id is None else request_id
         self.waiting.append((rid, [int(t) for t in prompt_ids]))
         self.params[rid] = params
@@ -239,6 +242,9 @@ class SpecEngine:
         from .engine import RequestOutput
         if not isinstance(params, list):
             params = [params or SamplingParams()] * len(prompts)
+        # one constraint per request, from its start
+        params = [dataclasses.replace(sp, constraint=sp.constraint.fresh())
+                  if sp is not None and sp.constraint is not None else sp for sp in params]
         rids = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
         res = {r: [] for r in rids}
         pending = set(rids)

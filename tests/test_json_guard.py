@@ -104,3 +104,72 @@ def test_responses_text_format_attaches_constraint():
         assert r.status_code == 200, r.text
     assert isinstance(seen[-1].constraint, JsonConstraint)
     ae.shutdown()
+
+
+def test_constrained_tree_walk_equals_plain_constrained_decoding():
+    """Speculative verify of a JSON reply: walking a draft tree with the
+    constraint applied at each node commits exactly what step-by-step
+    constrained decoding commits, while accepting drafted nodes."""
+    import numpy as np
+    import torch
+
+    from swarmllm_b200.engine.sampling import SamplingParams, constrained_token
+    from swarmllm_b200.engine.spec import walk_constrained
+    from swarmllm_b200.utils.ext import native
+    pieces = ['{', '}', '"a"', '"b"', ':', ', ', '1', '2', ' ', 'x', '[', ']', 'true', '"', 'ab']
+    EOS = len(pieces)
+    V = EOS + 1
+
+    def piece(t):
+        return pieces[t] if t < len(pieces) else ""
+
+    def logits(prefix):  # a deterministic stand-in for the target model
+        g = torch.Generator().manual_seed(hash(tuple(prefix)) % (2 ** 31))
+        return torch.randn(V, generator=g)
+
+    def choice(prefix):  # what plain constrained decoding commits after prefix
+        c = JsonConstraint(piece, EOS)
+        for t in prefix:
+            c.accept(t)
+        row = logits(prefix)
+        return constrained_token(c, int(row.argmax()), row, EOS)
+
+    plain = []
+    while len(plain) < 40 and (not plain or plain[-1] != EOS):
+        plain.append(choice(plain))
+
+    rng = np.random.default_rng(0)
+    c = JsonConstraint(piece, EOS)
+    row = logits([])
+    out = [constrained_token(c, int(row.argmax()), row, EOS)]
+    p = SamplingParams(eos_token_id=EOS, constraint=c)
+    accepted = 0
+    while len(out) < 40 and out[-1] != EOS:
+        tr = native().DraftTree(out[-1], 64)
+
+        def prefix_of(node):
+            par, tok, path = tr.parents(), tr.tokens(), []
+            while node != 0:
+                path.append(tok[node])
+                node = par[node]
+            return out + path[::-1]
+        for _ in range(3):
+            cand_t, cand_lp = [], []
+            for node in tr.frontier():
+                good = choice(prefix_of(node))
+                other = int(rng.integers(0, V))
+                first = good if rng.random() < 0.7 else other
+                cand_t += [first, other if other != first else (first + 1) % V]
+                cand_lp += [-0.1, -2.0]
+            tr.expand(cand_t, cand_lp, 2, 2)
+        n = len(tr)
+        rows = [logits(prefix_of(i)) for i in range(n)]
+        tgt = [int(r.argmax()) for r in rows]
+        path, bonus = walk_constrained(tr, tgt, rows, p)
+        accepted += len(path) - 1
+        toks = tr.tokens()
+        out += [toks[i] for i in path[1:]] + [bonus]
+    if EOS in out:
+        out = out[:out.index(EOS) + 1]
+    assert out[:len(plain)] == plain[:len(out)]
+    assert len(out) >= min(len(plain), 40) and accepted > 0
