@@ -165,9 +165,12 @@ class GgufSource:
         if self.cfg.arch == "glm4moe" and "swarmllm.config" not in self.f.metadata:
             # GLM-4.5 files say whether they carry q/k norms by the tensors alone
             self.cfg.qk_norm = "blk.0.attn_q_norm.weight" in self.f.tensors
-        # LongRoPE (phi3): per-pair frequency divisors stored as tensors; the
-        # short factors serve contexts up to the original training length
-        for name in ("rope_factors_short.weight", "rope_factors_long.weight"):
+        # per-pair frequency divisors stored as tensors: Llama 3.1-3.3 files
+        # carry their llama3 scaling as rope_freqs (each pair's angle divided
+        # by its factor; reference: split/loader/mod.rs load_rope_freqs);
+        # LongRoPE (phi3) as short / long factors, the short ones serving
+        # contexts up to the original training length
+        for name in ("rope_freqs.weight", "rope_factors_short.weight", "rope_factors_long.weight"):
             if self.cfg.rope_factors is None and name in self.f.tensors:
                 t, qt, shape = self.get(name)
                 self.cfg.rope_factors = Q.dequantize(t.numpy().reshape(-1), qt).tolist()

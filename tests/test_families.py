@@ -293,3 +293,32 @@ def test_gpu_model_refuses_unbuilt_options():
     for fam in ("llama4", "granite"):
         with pytest.raises(NotImplementedError, match=fam):
             LlamaGPU(family_cfg(fam), None, "cpu")
+
+
+def test_rope_freqs_tensor_scales_llama_rope(tmp_path):
+    """A Llama 3.x file's rope_freqs tensor (per-pair divisors, how llama3
+    scaling is stored) divides the rotary frequencies of the loaded model."""
+    from swarmllm_b200.gguf import quants as Q
+    from swarmllm_b200.gguf.file import GGUFWriter
+    from swarmllm_b200.models.config import rope_inv_freq, tiny_llama, to_gguf_metadata
+    from swarmllm_b200.models.layout import file_specs, to_file
+    from swarmllm_b200.models.weights import GgufSource, RandomSource, tensor_specs
+    cfg = tiny_llama()
+    src = RandomSource(cfg, seed=0)
+    w = GGUFWriter(cfg.arch)
+    md = to_gguf_metadata(cfg)
+    md.pop("swarmllm.config")
+    for k, v in md.items():
+        w.add(k, v)
+    for name, shape, qt in file_specs(cfg, tensor_specs(cfg)):
+        w.add_tensor(name, to_file(cfg, name, shape, qt, lambda n: src.get(n)[0].numpy()), qt, shape)
+    half = cfg.rot_dim // 2
+    factors = np.where(np.arange(half) < half // 2, 1.0, 8.0).astype(np.float32)
+    w.add_tensor("rope_freqs.weight", factors, Q.F32, (half,))
+    path = str(tmp_path / "l3.gguf")
+    w.write(path)
+    got = GgufSource(path).cfg
+    assert got.rope_factors == factors.tolist()
+    inv, _ = rope_inv_freq(got)
+    plain, _ = rope_inv_freq(cfg)
+    assert np.allclose(inv, plain / factors)
