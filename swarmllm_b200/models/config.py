@@ -401,6 +401,14 @@ def apply_family(cfg: ModelConfig, md: dict | None = None, prefix: str | None = 
     if fam == "gemma3":
         cfg.post_norms, cfg.qk_norm, cfg.swa_pattern = True, True, 6
         cfg.rope_local_theta = cfg.rope_local_theta or 10000.0
+    if md is not None and not cfg.attn_scale and (fam, cfg.n_layers) in (("gemma2", 46),
+                                                                      ("gemma3", 62)):
+        # the 27B members scale queries by 1/sqrt(hidden / heads), not
+        # 1/sqrt(head_dim) (query_pre_attn_scalar; the width in integers, as
+        # llama.cpp computes it).  Reference: split/gguf_meta.rs:570 query_scale.
+        width = cfg.hidden // cfg.n_heads
+        if width != cfg.head_dim and width > 0:
+            cfg.attn_scale = 1.0 / math.sqrt(width)
     if fam == "phi3":
         cfg.rope_neox, cfg.fused_qkv, cfg.fused_gate_up = True, True, True
     if fam == "glm4":

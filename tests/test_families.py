@@ -56,6 +56,11 @@ def test_family_options():
     c = from_gguf_metadata(md("gemma3", **{"attention.sliding_window": 1024}))
     assert c.qk_norm and c.swa_pattern == 6 and c.rope_local_theta == 10000.0
     assert [c.is_swa(i) for i in range(7)] == [True] * 5 + [False, True]
+    c = from_gguf_metadata({**md("gemma2"), "gemma2.block_count": 46, "gemma2.embedding_length": 4608,
+                            "gemma2.attention.head_count": 32, "gemma2.attention.key_length": 128})
+    assert abs(c.softmax_scale - 144 ** -0.5) < 1e-12          # Gemma 2 27B
+    c = from_gguf_metadata({**md("gemma3"), "gemma3.attention.key_length": 128})
+    assert abs(c.softmax_scale - 128 ** -0.5) < 1e-12          # other sizes: head width
     c = from_gguf_metadata(md("phi3"))
     assert c.fused_qkv and c.fused_gate_up
     c = from_gguf_metadata(md("glm4", **{"attention.key_length": 128}))
