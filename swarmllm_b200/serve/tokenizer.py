@@ -111,6 +111,7 @@ def pre_split(text: str, patterns) -> list[str]:
 
 
 class BPETokenizer:
+    adds_bos = True   # the file's rule, set by from_gguf_metadata (adds_bos)
     # fallback pre-tokenizer (Llama 3 style) when the regex module is missing
     PAT = re.compile(r"""'(?:[sdmt]|ll|ve|re)| ?[^\W\d_]+| ?\d{1,3}| ?[^\s\w]+[\r\n]*|\s*[\r\n]+|\s+(?!\S)|\s+""",
                      re.UNICODE)
@@ -159,7 +160,7 @@ class BPETokenizer:
         return ids
 
     def encode(self, text: str, add_bos: bool = True) -> list[int]:
-        ids = [self.bos_id] if (add_bos and self.bos_id >= 0) else []
+        ids = [self.bos_id] if (add_bos and self.adds_bos and self.bos_id >= 0) else []
         # split out special tokens first
         if self.special:
             pat = "(" + "|".join(re.escape(s) for s in sorted(self.special, key=len, reverse=True)) + ")"
@@ -205,6 +206,7 @@ class SPMTokenizer:
     list of symbols (O(n log n)); pieces outside the vocabulary fall back to
     byte tokens <0xNN>.  Control and user-defined tokens (token types 3 / 4)
     in the text are matched whole first, as the BPE tokenizer does."""
+    adds_bos = True   # the file's rule, set by from_gguf_metadata (adds_bos)
 
     def __init__(self, tokens: list[str], scores: list[float], bos_id: int = 1, eos_id: int = 2,
                  token_types: list[int] | None = None):
@@ -264,7 +266,7 @@ class SPMTokenizer:
         return ids
 
     def encode(self, text: str, add_bos: bool = True) -> list[int]:
-        ids = [self.bos_id] if add_bos and self.bos_id >= 0 else []
+        ids = [self.bos_id] if add_bos and self.adds_bos and self.bos_id >= 0 else []
         if self.special:
             pat = "(" + "|".join(re.escape(t) for t in sorted(self.special, key=len, reverse=True)) + ")"
             chunks = re.split(pat, text)
@@ -302,15 +304,41 @@ class SPMTokenizer:
         return self.decode([i])
 
 
+# BPE pre-tokenizers whose prompts start with BOS when the file does not say,
+# and those that never take one (llama.cpp's vocabulary rules)
+_PRE_ADD_BOS = {"llama3", "llama-v3", "llama-bpe", "falcon3", "falcon-h1", "pixtral", "midm-2.0",
+                "lfm2"}
+_PRE_NO_BOS = {"glm4", "chatglm-bpe"}
+
+
+def adds_bos(md: dict) -> bool:
+    """Whether a prompt starts with BOS: the file's tokenizer.ggml.add_bos_token
+    when present, else yes for a SentencePiece vocabulary and, for a GPT-2
+    BPE one, only for the pre-tokenizers that ask for it; a pre-tokenizer
+    without BOS overrides the key.  Qwen files, for one, name a BOS id but
+    declare add_bos_token false.  Reference: split/gguf_meta.rs:1374."""
+    model, pre = md.get("tokenizer.ggml.model"), md.get("tokenizer.ggml.pre", "")
+    if pre in _PRE_NO_BOS:
+        return False
+    declared = md.get("tokenizer.ggml.add_bos_token")
+    if declared is not None:
+        return bool(declared)
+    return model == "llama" or (model == "gpt2" and pre in _PRE_ADD_BOS)
+
+
 def from_gguf_metadata(md: dict, vocab_size: int):
     model = md.get("tokenizer.ggml.model")
     toks = md.get("tokenizer.ggml.tokens")
     bos = int(md.get("tokenizer.ggml.bos_token_id", -1))
     eos = int(md.get("tokenizer.ggml.eos_token_id", -1))
+    tok = None
     if toks and model == "gpt2":
-        return BPETokenizer(toks, md.get("tokenizer.ggml.merges", []), bos, eos,
-                            md.get("tokenizer.ggml.token_type"), md.get("tokenizer.ggml.pre"))
-    if toks and model == "llama":
-        return SPMTokenizer(toks, md.get("tokenizer.ggml.scores", [0.0] * len(toks)), bos, eos,
-                            md.get("tokenizer.ggml.token_type"))
-    return ByteTokenizer(vocab_size)
+        tok = BPETokenizer(toks, md.get("tokenizer.ggml.merges", []), bos, eos,
+                           md.get("tokenizer.ggml.token_type"), md.get("tokenizer.ggml.pre"))
+    elif toks and model == "llama":
+        tok = SPMTokenizer(toks, md.get("tokenizer.ggml.scores", [0.0] * len(toks)), bos, eos,
+                           md.get("tokenizer.ggml.token_type"))
+    if tok is None:
+        return ByteTokenizer(vocab_size)
+    tok.adds_bos = adds_bos(md)
+    return tok

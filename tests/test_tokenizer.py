@@ -83,3 +83,23 @@ def test_spm_special_tokens_stay_whole():
     ids = tok.encode("<start_of_turn>hi", add_bos=False)
     assert ids[0] == 3 and ids[1:] == [tok.vocab["hi"]]
     assert tok.encode("hi", add_bos=False) == [tok.vocab["▁hi"]]
+
+
+def test_bos_follows_the_files_rule():
+    """A prompt starts with BOS as llama.cpp decides it: the declared
+    add_bos_token, else SentencePiece yes, GPT-2 BPE only for the
+    pre-tokenizers that ask for it; GLM's pre-tokenizer never."""
+    from swarmllm_b200.serve.tokenizer import adds_bos, from_gguf_metadata
+    spm, bpe = {"tokenizer.ggml.model": "llama"}, {"tokenizer.ggml.model": "gpt2"}
+    assert adds_bos(spm) and not adds_bos({**spm, "tokenizer.ggml.add_bos_token": False})
+    assert not adds_bos({**bpe, "tokenizer.ggml.pre": "qwen2"})
+    assert adds_bos({**bpe, "tokenizer.ggml.pre": "llama-bpe"})
+    assert not adds_bos({**bpe, "tokenizer.ggml.pre": "glm4", "tokenizer.ggml.add_bos_token": True})
+    toks = ["<|endoftext|>", "a", "b", "ab"]
+    md = {**bpe, "tokenizer.ggml.pre": "qwen2", "tokenizer.ggml.tokens": toks,
+          "tokenizer.ggml.merges": ["a b"], "tokenizer.ggml.bos_token_id": 0,
+          "tokenizer.ggml.eos_token_id": 0, "tokenizer.ggml.add_bos_token": False}
+    tok = from_gguf_metadata(md, len(toks))
+    assert tok.encode("ab") == [3]
+    tok = from_gguf_metadata({**md, "tokenizer.ggml.add_bos_token": True}, len(toks))
+    assert tok.encode("ab") == [0, 3]
