@@ -8,6 +8,10 @@ import torch
 
 from test_families import FAMILIES, family_cfg
 
+# llama4 and granite's residual multiplier run on the CPU model only (the GPU
+# model refuses them by name: test_gpu_model_refuses_unbuilt_options)
+GPU_FAMILIES = [f for f in FAMILIES if f not in ("llama4", "granite")]
+
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 
@@ -19,7 +23,7 @@ def _batch(tokens, positions, bt, device, sample_rows):
                      t(sample_rows, torch.int64), 256)
 
 
-@pytest.mark.parametrize("fam", FAMILIES)
+@pytest.mark.parametrize("fam", GPU_FAMILIES)
 def test_family_gpu_matches_cpu_oracle(fam):
     from swarmllm_b200.models.llama import LlamaCPU, LlamaGPU
     from swarmllm_b200.models.weights import RandomSource
